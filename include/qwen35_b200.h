@@ -1,0 +1,114 @@
+/*
+ * C ABI of libqwen35_b200.so -- the B200 (sm_100a) implementation of the Qwen3.5 hybrid
+ * forward path behind lucebox-hub's torch-extension boundary.
+ *
+ * Every `launch_*` entry point has the argument list of the function of the same name that the
+ * reference's binding layer declares and calls (models/qwen35_0p8b/torch_bindings.cpp); the
+ * citation beside each declaration gives the lines.  Differences from the reference, all
+ * additive:
+ *   - every function returns an int status (0 = enqueued / ok) instead of void;
+ *   - `max_seq_len` is honoured (the reference hard-codes 2048 in its prefill);
+ *   - scratch arguments the reference kernels needed are accepted and ignored -- the library
+ *     keeps one private workspace per device, allocated on the first call on that device
+ *     (make that first call outside CUDA-graph capture).
+ * All pointers are device pointers unless stated otherwise.  Work is enqueued on `stream`; no
+ * entry point synchronises except qwen35_b200_status().
+ */
+#ifndef QWEN35_B200_H
+#define QWEN35_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* qwen35_stream_t; /* == cudaStream_t */
+
+/* Layer pointer records, layout of the reference (kernel.cu:77-115, torch_bindings.cpp:25-45). */
+typedef struct {
+    int layer_type;      /* 0 = DeltaNet (14 pointers), 1 = full attention (11 pointers) */
+    int _pad[3];
+    void* ptrs[14];      /* bf16 tensors in the order of models/qwen35_0p8b/model.py:342-380 */
+} LayerWeights;
+
+enum {
+    QWEN35_OK = 0,
+    QWEN35_ERR_BARRIER_TIMEOUT = 1, /* a bounded device-side wait ran out; state is undefined */
+    QWEN35_ERR_BAD_ARG = 2,
+    QWEN35_ERR_CUDA = 3,
+    QWEN35_ERR_UNSUPPORTED = 4
+};
+
+/* Replaces launch_decode (torch_bindings.cpp:47-60; kernel.cu:910-1020): one greedy decode step.
+ * Reads embed[input_token_id], runs 24 layers at `position`, appends K/V, updates the DeltaNet
+ * and conv state in place, writes arg-max(logits) to output_token_id[0].  The arg-max is taken
+ * over bf16-rounded logits and returns the lowest index among equal maxima. */
+int launch_decode(
+    int input_token_id, int* output_token_id,
+    const void* embed_weight, const LayerWeights* layer_weights,
+    const void* final_norm_weight, const void* lm_head_weight,
+    void* fa_k_cache, void* fa_v_cache,
+    void* dn_states, void* conv_bufs,
+    void* hidden_buffer, void* g_activations, void* g_residual,
+    void* g_qkv_scratch, void* g_kv_scratch, void* g_attn_out,
+    void* g_mlp_inter, void* g_z_scratch, void* g_beta_scratch,
+    void* g_alpha_scratch, void* g_normalized,
+    unsigned int* barrier_counter, unsigned int* barrier_generation,
+    float* block_max_vals, int* block_max_idxs,
+    unsigned int* lm_sync_counter,
+    int position, int max_seq_len, qwen35_stream_t stream);
+
+/* Extended decode / token-serial prefill.  No counterpart in the reference's BF16 path (its NVFP4
+ * path has the same idea in launch_decode_many_nvfp4, torch_bindings.cpp:87-102): runs `n_steps`
+ * steps in one launch, feeding each arg-max back on the device. */
+typedef struct {
+    const void* embed_weight;
+    const LayerWeights* layer_weights;
+    const void* final_norm_weight;
+    const void* lm_head_weight;
+    void* fa_k_cache;          /* bf16 [6][2][max_seq_len][256] */
+    void* fa_v_cache;
+    void* dn_states;           /* f32 [18][16][128 v][128 k] */
+    void* conv_bufs;           /* f32 [18][6144][4], newest input last */
+    const int* token_in;       /* device int: first input token; NULL -> token_imm */
+    int token_imm;
+    const int* forced_ids;     /* optional device [n_steps]: input of every step (prompt / teacher forcing) */
+    int* out_token;            /* optional device [1]: arg-max of the last step */
+    int* out_tokens;           /* optional device [n_steps]: arg-max of every step that ran the LM head */
+    float* logits_out;         /* optional device f32 [248320]: bf16-rounded logits of the last step */
+    void* hidden_out;          /* optional device bf16 [1024]: last layer output of the last step */
+    void* dbg_hidden;          /* optional device bf16 [24][1024]: every layer's output, last step */
+    const void* dbg_teacher;   /* optional device bf16 [24][1024]: layer l>0 reads row l as its input (layer-level parity tests) */
+    int position;
+    int max_seq_len;
+    int n_steps;
+    int lm_last_only;          /* 1 = run the LM head only after the last step */
+    int dbg_num_layers;        /* 0 = all 24; N>0 stops after N layers (debug) */
+} Qwen35DecodeArgs;
+
+int qwen35_b200_decode_steps(const Qwen35DecodeArgs* args, qwen35_stream_t stream);
+
+/* Synchronises `stream`, then returns the sticky device status word of the current device
+ * (QWEN35_OK, or the first error a kernel recorded).  qwen35_b200_clear_status() re-arms the
+ * library after an error. */
+int qwen35_b200_status(qwen35_stream_t stream);
+int qwen35_b200_clear_status(qwen35_stream_t stream);
+
+/* Debug: synchronise the device and copy one inter-stage vector of the workspace to the host.
+ * which: 0 = stage-A output (8224 bf16), 1 = DeltaNet core output (2048 bf16), 2 = hidden after the
+ * mixer residual (1024 bf16), 3 = silu(gate)*up (3584 bf16), 4 = layer output (1024 bf16). */
+int qwen35_b200_debug_read(int which, void* host_out);
+
+/* Copies the 32 RoPE inverse frequencies the kernels use to a host buffer (for tests). */
+int qwen35_b200_rope_inv_freq(float* host_out32);
+
+/* Number of kernels this library has launched in this process (bench bookkeeping). */
+long long qwen35_b200_launch_count(void);
+
+const char* qwen35_b200_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QWEN35_B200_H */

@@ -1,0 +1,77 @@
+// Per-device workspace, sticky status word and error reporting for libqwen35_b200.
+#include "runtime.h"
+
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
+#include "decode_bf16.cuh"
+
+namespace q35 {
+
+static constexpr int MAX_DEVICES = 64;
+static Workspace* g_ws[MAX_DEVICES] = {};
+static int g_sms[MAX_DEVICES] = {};
+static std::mutex g_mu;
+static thread_local char g_err[512] = "";
+std::atomic<long long> g_launches{0};
+
+void set_error(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+}
+
+Workspace* get_workspace() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) {
+        set_error("no current CUDA device");
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_ws[dev]) {
+        Workspace* p = nullptr;
+        cudaError_t e = cudaMalloc(&p, sizeof(Workspace));
+        if (e == cudaSuccess) e = cudaMemset(p, 0, sizeof(Workspace));
+        if (e != cudaSuccess) {
+            set_error("workspace allocation failed: %s", cudaGetErrorString(e));
+            return nullptr;
+        }
+        g_ws[dev] = p;
+    }
+    return g_ws[dev];
+}
+
+int device_sm_count() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) return 0;
+    if (!g_sms[dev]) cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    return g_sms[dev];
+}
+
+}  // namespace q35
+
+extern "C" int qwen35_b200_status(qwen35_stream_t stream) {
+    using namespace q35;
+    Workspace* ws = get_workspace();
+    if (!ws) return QWEN35_ERR_CUDA;
+    int err = 0;
+    Q35_CUDA_OK(cudaMemcpyAsync(&err, &ws->err, sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+    Q35_CUDA_OK(cudaStreamSynchronize((cudaStream_t)stream));
+    if (err) set_error("device status %d (%s)", err, err == 1 ? "a bounded device-side wait ran out" : "bad argument seen on device");
+    return err;
+}
+
+extern "C" int qwen35_b200_clear_status(qwen35_stream_t stream) {
+    using namespace q35;
+    Workspace* ws = get_workspace();
+    if (!ws) return QWEN35_ERR_CUDA;
+    // barrier counter, generation and status word restart from zero together
+    Q35_CUDA_OK(cudaMemsetAsync(ws, 0, 256, (cudaStream_t)stream));
+    return QWEN35_OK;
+}
+
+extern "C" long long qwen35_b200_launch_count(void) { return q35::g_launches.load(); }
+
+extern "C" const char* qwen35_b200_last_error(void) { return q35::g_err; }

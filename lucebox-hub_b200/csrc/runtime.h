@@ -1,0 +1,31 @@
+// Host-side runtime shared by the launchers: per-device workspace, status word, error text.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <atomic>
+
+#include "../../include/qwen35_b200.h"
+
+namespace q35 {
+
+struct Workspace;
+
+// Workspace of the current device; allocated and zeroed on first use (never inside a capture).
+// Returns nullptr and records an error string on failure.
+Workspace* get_workspace();
+
+int device_sm_count();
+void set_error(const char* fmt, ...);
+extern std::atomic<long long> g_launches;
+
+#define Q35_CUDA_OK(expr)                                                         \
+    do {                                                                          \
+        cudaError_t e__ = (expr);                                                 \
+        if (e__ != cudaSuccess) {                                                 \
+            q35::set_error("%s failed: %s", #expr, cudaGetErrorString(e__));      \
+            return QWEN35_ERR_CUDA;                                               \
+        }                                                                         \
+    } while (0)
+
+}  // namespace q35

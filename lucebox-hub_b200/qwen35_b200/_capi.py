@@ -1,0 +1,73 @@
+"""ctypes view of libqwen35_b200.so (declarations: include/qwen35_b200.h).
+
+There is no fallback: if the library is missing or a call fails, an exception is raised.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libqwen35_b200.so")
+
+OK = 0
+STATUS_NAMES = {0: "ok", 1: "device wait timed out", 2: "bad argument", 3: "CUDA error", 4: "unsupported"}
+
+
+class Qwen35Error(RuntimeError):
+    pass
+
+
+class DecodeArgs(C.Structure):
+    _fields_ = [
+        ("embed_weight", C.c_void_p), ("layer_weights", C.c_void_p),
+        ("final_norm_weight", C.c_void_p), ("lm_head_weight", C.c_void_p),
+        ("fa_k_cache", C.c_void_p), ("fa_v_cache", C.c_void_p),
+        ("dn_states", C.c_void_p), ("conv_bufs", C.c_void_p),
+        ("token_in", C.c_void_p), ("token_imm", C.c_int),
+        ("forced_ids", C.c_void_p), ("out_token", C.c_void_p), ("out_tokens", C.c_void_p),
+        ("logits_out", C.c_void_p), ("hidden_out", C.c_void_p), ("dbg_hidden", C.c_void_p), ("dbg_teacher", C.c_void_p),
+        ("position", C.c_int), ("max_seq_len", C.c_int), ("n_steps", C.c_int), ("lm_last_only", C.c_int), ("dbg_num_layers", C.c_int),
+    ]
+
+
+_lib = None
+
+# name -> (restype, argtypes); every symbol include/qwen35_b200.h declares
+_vp, _i = C.c_void_p, C.c_int
+SIGNATURES = {
+    "launch_decode": (_i, [_i, _vp] + [_vp] * 8 + [_vp] * 11 + [_vp] * 5 + [_i, _i, _vp]),
+    "qwen35_b200_decode_steps": (_i, [C.POINTER(DecodeArgs), _vp]),
+    "qwen35_b200_status": (_i, [_vp]),
+    "qwen35_b200_clear_status": (_i, [_vp]),
+    "qwen35_b200_debug_read": (_i, [_i, _vp]),
+    "qwen35_b200_rope_inv_freq": (_i, [C.POINTER(C.c_float)]),
+    "qwen35_b200_launch_count": (C.c_longlong, []),
+    "qwen35_b200_last_error": (C.c_char_p, []),
+}
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise Qwen35Error(
+                f"{LIB_PATH} is missing: build it with `python lucebox-hub_b200/build.py` "
+                "(there is no CPU or PyTorch fallback)")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(status: int, what: str):
+    if status != OK:
+        msg = lib().qwen35_b200_last_error().decode()
+        raise Qwen35Error(f"{what}: status {status} ({STATUS_NAMES.get(status, '?')}): {msg}")
+
+
+def ptr(t):
+    return None if t is None else t.data_ptr()

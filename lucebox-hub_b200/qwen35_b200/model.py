@@ -1,0 +1,227 @@
+"""Decode API for the B200 Qwen3.5-0.8B kernels -- a drop-in for the reference's
+`models/qwen35_0p8b/model.py`.
+
+Same names and meaning as the reference: the dimension constants (model.py:7-42), the
+`weights` dict (`embed_weight`, `final_norm_weight`, `lm_head_weight`, `layer_data`,
+model.py:386-391), `_pack_layer_weights` (128-byte layer records, model.py:410-427) and
+`class Decoder` with `step`, `step_many`, `prefill_tokens`, `reset`, `generate`
+(model.py:473-817).  State tensors have the reference's shapes and layouts so callers that
+reach into `_fa_k_cache`, `_dn_states`, `_conv_bufs`, `_hidden` keep working.
+
+Differences: `max_seq_len` is a constructor argument (the reference fixes 2048); `step_many`
+and `prefill_tokens` also work for the BF16 backend; with no checkpoint available weights
+come from `qwen35_b200.weights.make_random_weights`.  There is no CPU fallback: every call
+goes to libqwen35_b200.so and raises if it is missing or reports an error.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import struct
+
+import torch
+
+from . import _capi
+from .config import MAX_SEQ_LEN, QWEN35_0P8B
+
+_D = QWEN35_0P8B
+NUM_LAYERS = _D.num_layers
+HIDDEN_SIZE = _D.hidden
+INTERMEDIATE_SIZE = _D.intermediate
+VOCAB_SIZE = _D.vocab
+FA_NUM_Q_HEADS = _D.fa_q_heads
+FA_NUM_KV_HEADS = _D.fa_kv_heads
+FA_HEAD_DIM = _D.fa_head_dim
+FA_Q_SIZE = _D.fa_q_size
+FA_QPROJ_SIZE = _D.fa_qproj_size
+FA_KV_SIZE = _D.fa_kv_size
+DN_NUM_HEADS = _D.dn_heads
+DN_KEY_DIM = _D.dn_key_dim
+DN_VALUE_DIM = _D.dn_value_dim
+DN_QK_SIZE = _D.dn_qk_size
+DN_V_SIZE = _D.dn_v_size
+DN_CONV_CHANNELS = _D.dn_conv_channels
+DN_CONV_KERNEL = _D.dn_conv_kernel
+LAYER_TYPE = _D.layer_types
+
+
+def load_weights(model_name="random:1234", verbose=True, backend="bf16", device="cuda"):
+    """Reference signature (model.py:314-319).  Only `random:<seed>` sources exist here: no
+    checkpoint can be downloaded where this runs.  Returns (weights, tokenizer=None)."""
+    from .weights import make_random_weights, weights_to
+    if not str(model_name).startswith("random:"):
+        raise NotImplementedError(
+            "checkpoint loading needs files that are not available here; use 'random:<seed>'")
+    w = make_random_weights(int(str(model_name).split(":", 1)[1]), _D)
+    return weights_to(w, device), None
+
+
+def _pack_layer_weights(layer_data, device="cuda"):
+    """Device blob of 24 records {int type; int pad[3]; void* ptrs[14]} (model.py:410-427)."""
+    ptr_size, max_ptrs, header = 8, 14, 16
+    rec = header + max_ptrs * ptr_size
+    buf = bytearray(len(layer_data) * rec)
+    for i, ld in enumerate(layer_data):
+        off = i * rec
+        struct.pack_into("iiii", buf, off, ld["type"], 0, 0, 0)
+        for j, t in enumerate(ld["ptrs"]):
+            if t.dtype != torch.bfloat16 or not t.is_contiguous():
+                raise TypeError("layer tensors must be contiguous bf16")
+            struct.pack_into("Q", buf, off + header + j * ptr_size, t.data_ptr())
+    return torch.frombuffer(buf, dtype=torch.uint8).to(device)
+
+
+class Decoder:
+    """Stateful greedy decoder, batch 1 (reference: model.py:473)."""
+
+    def __init__(self, weights=None, tokenizer=None, model_name="random:1234", backend="bf16",
+                 verbose=False, max_seq_len=MAX_SEQ_LEN, device="cuda"):
+        if backend not in ("bf16", "auto", None):
+            raise ValueError(f"unsupported backend: {backend}")
+        self.backend = "bf16"
+        self.backend_label = "BF16"
+        self._lib = _capi.lib()
+        self.device = torch.device(device)
+        if weights is None:
+            weights, tokenizer = load_weights(model_name, verbose=verbose, device=device)
+        self.tokenizer = tokenizer
+        self.max_seq_len = int(max_seq_len)
+        self._position = 0
+        self._weights = weights
+        self._embed_weight = weights["embed_weight"]
+        self._final_norm_weight = weights["final_norm_weight"]
+        self._lm_head_weight = weights["lm_head_weight"]
+        self._layer_weights_packed = _pack_layer_weights(weights["layer_data"], device)
+
+        dev = self.device
+        n_fa = sum(1 for t in LAYER_TYPE if t == 1)
+        n_dn = NUM_LAYERS - n_fa
+        self._fa_k_cache = torch.zeros(n_fa, FA_NUM_KV_HEADS, self.max_seq_len, FA_HEAD_DIM, dtype=torch.bfloat16, device=dev)
+        self._fa_v_cache = torch.zeros_like(self._fa_k_cache)
+        # [layer][head][v][k] f32 -- value-major like the reference kernels (kernel.cu:684)
+        self._dn_states = torch.zeros(n_dn, DN_NUM_HEADS, DN_VALUE_DIM, DN_KEY_DIM, dtype=torch.float32, device=dev)
+        self._conv_bufs = torch.zeros(n_dn, DN_CONV_CHANNELS, DN_CONV_KERNEL, dtype=torch.float32, device=dev)
+        self._hidden = torch.empty(HIDDEN_SIZE, dtype=torch.bfloat16, device=dev)
+        self._out_token = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._token_buf = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    # ---- helpers ---------------------------------------------------------------------------
+    def _stream(self):
+        return C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+
+    def _args(self, **kw):
+        a = _capi.DecodeArgs()
+        a.embed_weight = self._embed_weight.data_ptr()
+        a.layer_weights = self._layer_weights_packed.data_ptr()
+        a.final_norm_weight = self._final_norm_weight.data_ptr()
+        a.lm_head_weight = self._lm_head_weight.data_ptr()
+        a.fa_k_cache = self._fa_k_cache.data_ptr()
+        a.fa_v_cache = self._fa_v_cache.data_ptr()
+        a.dn_states = self._dn_states.data_ptr()
+        a.conv_bufs = self._conv_bufs.data_ptr()
+        a.hidden_out = self._hidden.data_ptr()
+        a.out_token = self._out_token.data_ptr()
+        a.position = self._position
+        a.max_seq_len = self.max_seq_len
+        for k, v in kw.items():
+            setattr(a, k, v)
+        return a
+
+    def _run(self, a):
+        with torch.cuda.device(self.device):
+            _capi.check(self._lib.qwen35_b200_decode_steps(C.byref(a), self._stream()), "decode")
+
+    def check_status(self):
+        """Synchronise and raise if a kernel recorded an error (e.g. a bounded wait ran out)."""
+        with torch.cuda.device(self.device):
+            _capi.check(self._lib.qwen35_b200_status(self._stream()), "device status")
+
+    # ---- reference API -----------------------------------------------------------------------
+    def step(self, token_id: int) -> int:
+        """Decode one token, return the next token id (model.py:678-714; one D2H sync)."""
+        with torch.cuda.device(self.device):
+            none = None
+            _capi.check(self._lib.launch_decode(
+                int(token_id), self._out_token.data_ptr(),
+                self._embed_weight.data_ptr(), self._layer_weights_packed.data_ptr(),
+                self._final_norm_weight.data_ptr(), self._lm_head_weight.data_ptr(),
+                self._fa_k_cache.data_ptr(), self._fa_v_cache.data_ptr(),
+                self._dn_states.data_ptr(), self._conv_bufs.data_ptr(),
+                self._hidden.data_ptr(), *([none] * 10), *([none] * 5),
+                self._position, self.max_seq_len, self._stream()), "launch_decode")
+        self._position += 1
+        return int(self._out_token.item())
+
+    def step_many(self, token_id: int, num_steps: int, logits_out=None) -> torch.Tensor:
+        """`num_steps` greedy steps in one launch, tokens fed back on the device
+        (model.py:716-743 offers this for NVFP4 only).  Returns int32 [num_steps] on the GPU."""
+        if num_steps < 0:
+            raise ValueError("num_steps must be non-negative")
+        out = torch.empty(num_steps, dtype=torch.int32, device=self.device)
+        if num_steps == 0:
+            return out
+        a = self._args(token_imm=int(token_id), n_steps=num_steps, out_tokens=out.data_ptr(),
+                       logits_out=_capi.ptr(logits_out))
+        self._run(a)
+        self._position += num_steps
+        return out
+
+    def prefill_tokens(self, token_ids: torch.Tensor, logits_out=None) -> int:
+        """Reset, run the prompt, return the first generated token (model.py:745-799)."""
+        if token_ids.device.type != "cuda" or token_ids.dtype != torch.int32 or token_ids.dim() != 1:
+            raise TypeError("token_ids must be a 1D CUDA int32 tensor")
+        self.reset()
+        n = int(token_ids.numel())
+        if n == 0:
+            raise ValueError("empty prompt")
+        a = self._args(forced_ids=token_ids.data_ptr(), n_steps=n, lm_last_only=1,
+                       logits_out=_capi.ptr(logits_out))
+        self._run(a)
+        self._position = n
+        return int(self._out_token.item())
+
+    def forced_steps(self, token_ids: torch.Tensor, logits_out=None, dbg_hidden=None, dbg_teacher=None,
+                     dbg_num_layers=0) -> torch.Tensor:
+        """Teacher-forced decode: feed `token_ids` one per step, return the arg-max of every step."""
+        n = int(token_ids.numel())
+        out = torch.empty(n, dtype=torch.int32, device=self.device)
+        a = self._args(forced_ids=token_ids.data_ptr(), n_steps=n, out_tokens=out.data_ptr(),
+                       logits_out=_capi.ptr(logits_out), dbg_hidden=_capi.ptr(dbg_hidden),
+                       dbg_teacher=_capi.ptr(dbg_teacher), dbg_num_layers=dbg_num_layers)
+        self._run(a)
+        self._position += n
+        return out
+
+    def debug_read(self, which: str) -> torch.Tensor:
+        """Inter-stage vector of the library workspace (bf16, CPU): 'xa', 'o', 'h1', 'm', 'h2'."""
+        idx, n = {"xa": (0, 8224), "o": (1, 2048), "h1": (2, 1024), "m": (3, 3584), "h2": (4, 1024)}[which]
+        out = torch.empty(n, dtype=torch.bfloat16)
+        with torch.cuda.device(self.device):
+            _capi.check(self._lib.qwen35_b200_debug_read(idx, out.data_ptr()), "debug_read")
+        return out
+
+    def reset(self):
+        self._position = 0
+        self._fa_k_cache.zero_()
+        self._fa_v_cache.zero_()
+        self._dn_states.zero_()
+        self._conv_bufs.zero_()
+
+    def generate(self, prompt, max_tokens: int = 100):
+        """Greedy generation.  `prompt` is a string when a tokenizer is attached (reference
+        behaviour, model.py:804-817) or a sequence of token ids; returns text or ids."""
+        if isinstance(prompt, str):
+            if self.tokenizer is None:
+                raise RuntimeError("no tokenizer attached; pass token ids")
+            ids = self.tokenizer.encode(prompt, add_special_tokens=True)
+        else:
+            ids = [int(t) for t in prompt]
+        first = self.prefill_tokens(torch.tensor(ids, dtype=torch.int32, device=self.device))
+        out = [first]
+        if max_tokens > 1:
+            out += self.step_many(first, max_tokens - 1).tolist()
+        if isinstance(prompt, str):
+            eos = self.tokenizer.eos_token_id
+            if eos in out:
+                out = out[:out.index(eos)]
+            return self.tokenizer.decode(out, skip_special_tokens=True)
+        return out

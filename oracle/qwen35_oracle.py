@@ -174,6 +174,7 @@ class Oracle:
         self.k_cache = [None] * d.n_fa
         self.v_cache = [None] * d.n_fa
         self.last_hidden = None      # [S, hidden] bf16, output of the last layer (pre final norm)
+        self.trace = []              # per layer: output hidden of the last position of the last call
 
     # ---- layer bodies -------------------------------------------------------------------
     def _deltanet(self, i_dn: int, p: list, x: torch.Tensor, use_state: bool) -> torch.Tensor:
@@ -254,6 +255,7 @@ class Oracle:
         pos = torch.arange(self.position, self.position + S)
         cos, sin = rope_tables(pos, d.fa_rotary_dim, d.rope_theta, h.dtype)
         i_dn = i_fa = 0
+        self.trace = []
         for ld in self.w["layer_data"]:
             p = ld["ptrs"]
             x = rmsnorm(h, p[0], d.rms_eps)
@@ -268,6 +270,7 @@ class Oracle:
             h = h + y
             x = rmsnorm(h, post, d.rms_eps)
             h = h + F.linear(F.silu(F.linear(x, gate_w)) * F.linear(x, up_w), down_w)
+            self.trace.append(h[-1])
         self.position += S
         self.last_hidden = h
         return h
