@@ -1,0 +1,335 @@
+#!/usr/bin/env python
+"""Benchmark of the Qwen3.5-0.8B hybrid forward path on B200 (one JSON line on stdout).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: Qwen3.5-0.8B-architecture, seeded random-init BF16 weights, batch 1, a 520-token
+uniform-random prompt, then 128 greedy decode tokens (the reference's pp520 / tg128 benchmark,
+models/qwen35_0p8b/final_bench.py:158-238, with synthetic weights and ids).  One "step" is one
+tg128 run: the post-prefill state is restored on the device, then 128 tokens are decoded.
+  value  decode tok/s over all ranks, tokens and state resident in HBM (one launch per step)
+  e2e    the same through Decoder.step(), one launch + one device->host read per token
+Multi-GPU: one process per GPU (torchrun), weights replicated, one independent sequence per
+rank, no collective inside the timed region ("weak" scaling); NCCL only carries the barrier and
+the max-over-ranks of the elapsed time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "lucebox-hub_b200"))
+
+import torch  # noqa: E402
+
+PROMPT = 520
+GEN = 128
+
+
+def workload_config(world: int) -> dict:
+    return {"workload": "qwen35-0.8b-arch random-init bf16, bs=1 per GPU, pp%d + tg%d greedy (BASELINE configs[0])" % (PROMPT, GEN),
+            "prompt_tokens": PROMPT, "gen_tokens": GEN, "sequences_per_gpu": 1,
+            "l2": "per-token working set 1.5 GB of weights >> 126 MB L2 (no flush needed)",
+            "parallelism": f"replicas x{world}, no collectives"}
+
+BASELINE_TG128 = 711.0       # reference BF16 megakernel tg128 on B200
+BASELINE_PP520 = 40278.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def decode_bytes(position: int) -> int:
+    """Algorithmic HBM bytes of one bs=1 BF16 decode token at context length position+1:
+    all weights once, embedding row, DeltaNet state and conv state read+write, K/V read of the
+    whole context + one K/V row written."""
+    weights = 2 * (498_113_344 + 254_279_680)
+    state = 2 * 18 * 16 * 128 * 128 * 4
+    conv = 2 * 18 * 6144 * 4 * 4
+    kv_row = 6 * 2 * 2 * 256 * 2
+    return weights + 2048 + state + conv + kv_row * (position + 1) + kv_row
+
+
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200", "-i", str(self.idx)],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        try:
+            out, _ = self.p.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+            out, _ = self.p.communicate()
+        sm, mx, reasons = [], [], set()
+        for line in out.splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1])); mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(weights_cpu, ids, n_decode=16, use_hf=False):
+    """The reference's CPU path on the host cores: one pp520 forward + `n_decode` cached greedy
+    steps.  use_hf=True runs the installed transformers model itself, else the oracle port."""
+    from qwen35_b200.config import QWEN35_0P8B as D
+    cores = host_cores()
+    torch.set_num_threads(cores)
+    if use_hf:
+        from oracle.hf_reference import build_hf, greedy
+        model = build_hf(weights_cpu, D)
+        _, _, _, t_pp, t_tg = greedy(model, ids, n_decode + 1)
+        kind = "reference"
+    else:
+        from oracle.qwen35_oracle import Oracle
+        o = Oracle(weights_cpu, D, 2048)
+        t0 = time.perf_counter()
+        lg = o.prefill(ids)
+        t1 = time.perf_counter()
+        for _ in range(n_decode):
+            lg = o.step(int(lg.argmax()))
+        t_pp, t_tg = t1 - t0, time.perf_counter() - t1
+        kind = "port"
+    return {"value": n_decode / t_tg, "unit": "tok/s", "cores": cores, "kind": kind,
+            "sample": f"pp{PROMPT} once ({PROMPT / t_pp:.1f} tok/s) + {n_decode} greedy decode steps, bf16, torch CPU",
+            "pp520_tok_s": PROMPT / t_pp}
+
+
+def run_reference(args):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return
+    from qwen35_b200.config import QWEN35_0P8B as D
+    from qwen35_b200.weights import make_random_weights, make_token_ids
+    w = make_random_weights(1234, D)
+    ids = make_token_ids(PROMPT, 7, D.vocab)
+    try:
+        import transformers  # noqa: F401
+        use_hf = True
+    except Exception:
+        use_hf = False
+    n_dec = 16
+    vals, pps = [], []
+    base = None
+    t_start = time.perf_counter()
+    for i in range(args.warmup + args.steps):
+        base = cpu_baseline(w, ids, n_dec, use_hf)
+        if i >= args.warmup:
+            vals.append(base["value"]); pps.append(base["pp520_tok_s"])
+        if time.perf_counter() - t_start > 240 and vals:
+            break
+    v = sum(vals) / len(vals)
+    base["value"] = v
+    line = {"impl": "reference", "metric": "decode_tg%d_tok_s" % GEN, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": len(vals), "warmup": args.warmup, "ms_per_step": 1e3 * n_dec / v, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": workload_config(args.gpus), "sample": "each step = one pp%d forward + a %d-token greedy decode sample on the host cores" % (PROMPT, n_dec),
+            "pp520_tok_s": sum(pps) / len(pps), "cpu_baseline": base,
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def run_ours(args):
+    rank, local_rank, world = dist_env()
+    from qwen35_b200 import _capi
+    from qwen35_b200.config import QWEN35_0P8B as D
+    from qwen35_b200.model import Decoder
+    from qwen35_b200.weights import make_random_weights, make_token_ids, weights_to
+
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (there is no CPU fallback)")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+
+    w_cpu = make_random_weights(1234, D)
+    wg = weights_to(w_cpu, dev)
+    dec = Decoder(weights=wg, max_seq_len=2048, device=dev)
+    ids_cpu = make_token_ids(PROMPT, 7 + rank, D.vocab)
+    ids = ids_cpu.pin_memory().to(dev, non_blocking=True)
+    lib = _capi.lib()
+
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+
+    # ---- prefill (pp520), timed separately ----
+    pp_ms = []
+    for i in range(3):
+        e0, e1 = ev(), ev()
+        e0.record()
+        first = dec.prefill_tokens(ids)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        pp_ms.append(e0.elapsed_time(e1))
+    dec.check_status()
+    snap = [t.clone() for t in (dec._fa_k_cache, dec._fa_v_cache, dec._dn_states, dec._conv_bufs)]
+
+    def restore():
+        for dst, src in zip((dec._fa_k_cache, dec._fa_v_cache, dec._dn_states, dec._conv_bufs), snap):
+            dst.copy_(src, non_blocking=True)
+        dec._position = PROMPT
+
+    def step_device():
+        restore()
+        return dec.step_many(first, GEN)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(max(args.warmup, 3)):
+        step_device()
+    barrier()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    launches0 = lib.qwen35_b200_launch_count()
+    k_ev = []
+    barrier()
+    t0, t1 = ev(), ev()
+    t0.record()
+    for _ in range(args.steps):
+        restore()
+        a, b = ev(), ev()
+        a.record()
+        toks = dec.step_many(first, GEN)
+        b.record()
+        k_ev.append((a, b))
+    t1.record()
+    barrier()
+    launches = lib.qwen35_b200_launch_count() - launches0
+    total_ms = t0.elapsed_time(t1)
+    kernel_ms = [a.elapsed_time(b) for a, b in k_ev]
+
+    # ---- e2e: the reference's host loop, Decoder.step() with one D2H read per token ----
+    e2e_steps = max(1, min(args.steps, 3))
+    restore(); tok = first
+    for _ in range(8):
+        tok = dec.step(tok)
+    barrier()
+    tw0 = time.perf_counter()
+    e0, e1 = ev(), ev()
+    e0.record()
+    for _ in range(e2e_steps):
+        restore(); tok = first
+        for _ in range(GEN):
+            tok = dec.step(tok)
+    e1.record()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    clocks = sampler.stop()
+    dec.check_status()
+
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([total_ms, e2e_ms, sum(kernel_ms) / len(kernel_ms)], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_ms, kern_avg = t.tolist()
+        cnt = torch.tensor([launches], dtype=torch.int64, device=dev)
+        dist.all_reduce(cnt)
+        launches = int(cnt.item())
+    else:
+        kern_avg = sum(kernel_ms) / len(kernel_ms)
+
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        value = world * GEN * args.steps / (total_ms * 1e-3)
+        alg_bytes = sum(decode_bytes(PROMPT + i) for i in range(GEN))
+        achieved = alg_bytes / (kern_avg * 1e-3) / 1e9
+        traffic = None
+        try:
+            with open(os.path.join(ROOT, "profiles", "decode_bf16_traffic.json")) as f:
+                traffic = json.load(f).get("dram_bytes_per_launch_tg128")
+        except Exception:
+            pass
+        line = {
+            "metric": "decode_tg%d_tok_s" % GEN, "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": (value / BASELINE_TG128) if (world == 1 and GEN == 128 and PROMPT == 520) else None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": workload_config(world),
+            "pp520_tok_s": PROMPT / (min(pp_ms) * 1e-3), "pp520_ms": min(pp_ms),
+            "pp520_vs_baseline": PROMPT / (min(pp_ms) * 1e-3) / BASELINE_PP520,
+            "pp520_note": "token-serial prefill through the decode megakernel",
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "traffic": traffic, "kernel": "decode_bf16_kernel",
+                         "algorithmic_bytes_per_launch": alg_bytes, "launch_ms": kern_avg},
+            "e2e": {"value": world * GEN * e2e_steps / (e2e_ms * 1e-3), "unit": "tok/s",
+                    "h2d_bytes_per_step": GEN * 4, "d2h_bytes_per_step": GEN * 4,
+                    "path": "Decoder.step(): one launch_decode + one 4-byte device->host read per token"},
+            "gpu_launches": launches, "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(w_cpu, ids_cpu, 16, use_hf=False)
+        print(json.dumps(line))
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prompt", type=int, default=520, help="prompt tokens (smaller values are for profiler captures)")
+    ap.add_argument("--gen", type=int, default=128, help="decode tokens per step")
+    args = ap.parse_args()
+    global PROMPT, GEN
+    PROMPT, GEN = args.prompt, args.gen
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()
