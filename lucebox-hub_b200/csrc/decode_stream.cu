@@ -1,0 +1,806 @@
+// Streaming BF16 decode megakernel for the Qwen3.5-0.8B hybrid network (sm_100a).
+//
+// Replaces models/qwen35_0p8b/kernel.cu of the reference (decode_kernel :820-904, the layer
+// bodies :409-741, lm_head_kernel :747-814, launch_decode :910-1020).  One persistent
+// cooperative launch (one CTA per SM) runs all 24 layers and the LM-head arg-max for one or
+// many tokens.  Per CTA:
+//   * warp 16 is a TMA producer.  It walks this CTA's static list of weight tiles (16 KB,
+//     contiguous rows of one matrix) for every stage of every layer and keeps a 12-slot
+//     shared-memory ring full with cp.async.bulk copies, never waiting for activations, so HBM
+//     keeps streaming while the consumers wait for the previous stage;
+//   * warps 0-15 are consumers.  A stage waits for its input vector by polling flagged 64-bit
+//     words {two bf16, epoch} that the previous stage's CTAs wrote straight to L2, computes its
+//     rows from shared memory, and publishes its outputs the same way.  There is no grid
+//     barrier anywhere on the path.
+// Stages per layer: A input norm + fused projection; B DeltaNet recurrence (all CTAs, one warp
+// per pair of value rows) or attention (B1 scores, B2 P.V partials, B3 merge+gate on a few
+// CTAs); C gated norm / copy + output projection + residual; D post norm + gate/up with
+// SiLU*up; E down projection + residual.  Numerics are those of a bf16 HuggingFace model.
+#include "decode_stream.cuh"
+
+#include <cooperative_groups.h>
+
+namespace q35 {
+
+// 1 / theta^(2i/64), i = 0..31, theta = 1e7 (the reference evaluates powf per call, kernel.cu:483-490);
+// filled by the host from a double-precision pow so that it equals torch's f32 table bit for bit.
+__constant__ float c_rope_inv_freq[FA_ROT / 2];
+
+struct Smem {
+    // ring first: 16-byte aligned slots
+    unsigned char ring[NSLOTS * SLOT_BYTES];
+    unsigned long long full[NSLOTS];
+    unsigned long long empty[NSLOTS];
+    LayerRec layers[NUM_LAYERS];
+    __align__(16) bf16 x[INTER];                 // GEMV input of the current stage
+    __align__(16) bf16 h[HIDDEN];                // raw layer input (residual of stage C)
+    __align__(16) bf16 h1[HIDDEN];               // raw mixer output (residual of stage E)
+    float part[256];
+    float red[NCONS_WARPS];
+    __align__(16) float qk[2][2][DN_K];
+    float hd[2][2];
+    __align__(16) float q[FA_GQA][FA_HEAD_DIM];
+    __align__(16) float kcur[FA_HEAD_DIM];
+    float p[FA_GQA][256];
+    float ml[FA_GQA][2];
+    int abort_flag;
+    int tok;
+};
+
+__device__ __forceinline__ unsigned epoch_of(const DecodeArgs& a, int step, int slot) {
+    return a.epoch_base + 32u * (unsigned)step + (unsigned)slot + 1u;   // slot: 0..23 layer, 24 LM
+}
+
+// ------------------------------------------------------------------------------------------------
+// producer: issue every weight tile of this CTA in consumption order
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void produce(const DecodeArgs& a, Smem& s, Ring ring, const Abort& ab) {
+    const int b = blockIdx.x, G = gridDim.x;
+    const u64 pol = l2_policy_evict_first();
+    auto issue = [&](const void* src, uint32_t bytes) {
+        if (ab.on()) return;                       // after an abort nothing new is put in flight
+        const unsigned t = ring.t;
+        mbar_wait(ring.empty_bar(t), ring.phase(t) ^ 1u, ab);
+        if (ab.on()) return;
+        ring.t = t + 1;
+        mbar_arrive_expect_tx(ring.full_bar(t), bytes);
+        tma_load_1d(ring.slot_addr(t), src, bytes, ring.full_bar(t), pol);
+    };
+    const int n_layers = a.dbg_num_layers > 0 ? a.dbg_num_layers : NUM_LAYERS;
+    for (int step = 0; step < a.n_steps; ++step) {
+        for (int layer = 0; layer < n_layers; ++layer) {
+            const LayerRec& L = s.layers[layer];
+            const char *w_out, *w_gate, *w_up, *w_down;
+            if (L.type == 0) {
+                const char* wqkv = (const char*)L.p[DN_QKV]; const char* wz = (const char*)L.p[DN_Z];
+                const char* wb = (const char*)L.p[DN_B];     const char* wa = (const char*)L.p[DN_A];
+                for (int u = part_begin(TILES_A_DN, b, G); u < part_begin(TILES_A_DN, b + 1, G); ++u) {
+                    const int v = u * 8;
+                    const char* src = v < DN_CONV_CH ? wqkv + (size_t)v * 2048
+                                    : v < DN_CONV_CH + DN_V_SIZE ? wz + (size_t)(v - DN_CONV_CH) * 2048
+                                    : v < DN_CONV_CH + DN_V_SIZE + DN_HEADS ? wb + (size_t)(v - DN_CONV_CH - DN_V_SIZE) * 2048
+                                    : wa + (size_t)(v - DN_CONV_CH - DN_V_SIZE - DN_HEADS) * 2048;
+                    issue(src, SLOT_BYTES);
+                }
+                w_out = (const char*)L.p[DN_OUT]; w_gate = (const char*)L.p[DN_GATE]; w_up = (const char*)L.p[DN_UP]; w_down = (const char*)L.p[DN_DOWN];
+            } else {
+                const char* wq = (const char*)L.p[FA_Q]; const char* wk = (const char*)L.p[FA_K]; const char* wv = (const char*)L.p[FA_V];
+                for (int u = part_begin(TILES_A_FA, b, G); u < part_begin(TILES_A_FA, b + 1, G); ++u) {
+                    const int v = u * 8;
+                    const char* src = v < FA_QPROJ ? wq + (size_t)v * 2048
+                                    : v < FA_QPROJ + FA_KV_SIZE ? wk + (size_t)(v - FA_QPROJ) * 2048
+                                    : wv + (size_t)(v - FA_QPROJ - FA_KV_SIZE) * 2048;
+                    issue(src, SLOT_BYTES);
+                }
+                w_out = (const char*)L.p[FA_O]; w_gate = (const char*)L.p[FA_GATE]; w_up = (const char*)L.p[FA_UP]; w_down = (const char*)L.p[FA_DOWN];
+            }
+            for (int u = part_begin(TILES_C, b, G); u < part_begin(TILES_C, b + 1, G); ++u) issue(w_out + (size_t)u * SLOT_BYTES, SLOT_BYTES);
+            for (int u = part_begin(UNITS_D, b, G); u < part_begin(UNITS_D, b + 1, G); ++u) {
+                issue(w_gate + (size_t)u * SLOT_BYTES, SLOT_BYTES);
+                issue(w_up + (size_t)u * SLOT_BYTES, SLOT_BYTES);
+            }
+            for (int u = part_begin(TILES_E, b, G); u < part_begin(TILES_E, b + 1, G); ++u) issue(w_down + (size_t)u * 14336, 14336);
+        }
+        if (!a.lm_last_only || step == a.n_steps - 1)
+            for (int u = part_begin(TILES_LM, b, G); u < part_begin(TILES_LM, b + 1, G); ++u)
+                issue((const char*)a.lm_head + (size_t)u * SLOT_BYTES, SLOT_BYTES);
+    }
+    // drain: every copy this CTA issued must have landed before the CTA may exit
+    const unsigned issued = ring.t;
+    const unsigned first = issued > NSLOTS ? issued - NSLOTS : 0;
+    for (unsigned t = first; t < issued; ++t) {
+        unsigned it = 0;
+        while (!mbar_try_wait(ring.full_bar(t), ring.phase(t))) {
+            if (++it > POLL_LIMIT) { ab.raise(ERR_BARRIER_TIMEOUT); break; }
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// consumer helpers
+// ------------------------------------------------------------------------------------------------
+// K = 1024 rows, 8 per tile: four tiles in flight per CTA, warp w takes tile w/4, rows 2(w%4), +1.
+// NMAT = 2 pairs a gate tile with an up tile.  epi(first_row_of_pair, sums[NMAT][2]) runs on lane 0.
+template <int NMAT, typename Epi>
+__device__ __forceinline__ void consume_k1024(Ring& ring, int n_units, const bf16* xs, const Abort& ab, Epi epi) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float x[32];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) unpack8(*reinterpret_cast<const uint4*>(xs + (j * 32 + lane) * 8), x + 8 * j);
+    const unsigned t0 = ring.t;
+    for (int g = 0; g < n_units; g += 4) {
+        const int ui = g + (warp >> 2);
+        if (ui < n_units) {
+            float acc[NMAT][2];
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) {
+                const unsigned tile = t0 + (unsigned)(ui * NMAT + m);
+                mbar_wait(ring.full_bar(tile), ring.phase(tile), ab);
+                const uint32_t base = ring.slot_addr(tile) + (uint32_t)(2 * (warp & 3)) * 2048u + (uint32_t)lane * 16u;
+                uint4 w0[4], w1[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) { w0[j] = lds128(base + j * 512); w1[j] = lds128(base + 2048 + j * 512); }
+                float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) { a0 = dot8(w0[j], x + 8 * j, a0); a1 = dot8(w1[j], x + 8 * j, a1); }
+                acc[m][0] = warp_sum(a0);
+                acc[m][1] = warp_sum(a1);
+                if (lane == 0) mbar_arrive(ring.empty_bar(tile), 4);
+            }
+            if (lane == 0) epi(ui * 8 + 2 * (warp & 3), acc);
+        }
+    }
+    ring.t = t0 + (unsigned)(n_units * NMAT);
+}
+
+__device__ __forceinline__ void poll2(const u64* p0, const u64* p1, uint32_t epoch, const Abort& ab, uint32_t& o0, uint32_t& o1) {
+    const u64 v0 = ld_word(p0), v1 = ld_word(p1);
+    o0 = ((uint32_t)(v0 >> 32) == epoch) ? (uint32_t)v0 : poll_word(p0, epoch, ab);
+    o1 = ((uint32_t)(v1 >> 32) == epoch) ? (uint32_t)v1 : poll_word(p1, epoch, ab);
+}
+
+// RMSNorm(1+w) of 1024 values held one pair per consumer thread; writes bf16 to xs.
+__device__ __forceinline__ void rmsnorm_pair(uint32_t raw, const bf16* w, bf16* xs, float* s_red) {
+    const int t = threadIdx.x;
+    const float x0 = bf_lo(raw), x1 = bf_hi(raw);
+    const float tot = cons_block_sum(x0 * x0 + x1 * x1, s_red);
+    const float r = rsqrt_ieee(tot * (1.0f / HIDDEN) + RMS_EPS);
+    const uint32_t wr = __ldg(reinterpret_cast<const uint32_t*>(w) + t);
+    reinterpret_cast<uint32_t*>(xs)[t] = pack_bf16x2((x0 * r) * (1.0f + bf_lo(wr)), (x1 * r) * (1.0f + bf_hi(wr)));
+}
+
+// ------------------------------------------------------------------------------------------------
+// kernel
+// ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const DecodeArgs a) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    Smem& s = *reinterpret_cast<Smem*>(smem_raw);
+    StreamWorkspace* ws = a.ws;
+    const int b = blockIdx.x, G = gridDim.x;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    if (tid == 0) s.abort_flag = (ld_volatile(&ws->err) != 0) ? 1 : 0;
+    __syncthreads();
+    if (s.abort_flag) return;                 // sticky error from an earlier launch: the whole CTA leaves before touching the ring
+    if (tid == 0) {
+        for (int i = 0; i < NSLOTS; ++i) {
+            mbar_init(smem_u32(&s.full[i]), 1);
+            mbar_init(smem_u32(&s.empty[i]), NCONS_WARPS);
+        }
+        mbar_fence_init();
+    }
+    for (int i = tid; i < NUM_LAYERS * (int)(sizeof(LayerRec) / 16); i += STREAM_THREADS)
+        reinterpret_cast<uint4*>(s.layers)[i] = __ldg(reinterpret_cast<const uint4*>(a.layers) + i);
+    __syncthreads();
+
+    Abort ab{&s.abort_flag, &ws->err};
+    Ring ring{smem_u32(s.ring), smem_u32(s.full), smem_u32(s.empty), 0u};
+
+    if (warp == NCONS_WARPS) {
+        if (lane == 0) produce(a, s, ring, ab);
+        __syncwarp();
+    } else {
+        // =========================== consumers ===========================
+        int tok = a.token_in ? __ldg(a.token_in) : a.token_imm;
+        const int n_layers = a.dbg_num_layers > 0 ? a.dbg_num_layers : NUM_LAYERS;
+        for (int step = 0; step < a.n_steps; ++step) {
+            if (a.forced_ids) tok = __ldg(a.forced_ids + step);
+            if (tok < 0 || tok >= VOCAB) { if (tid == 0) atomicCAS(&ws->err, 0, (int)ERR_BAD_ARG); tok = 0; }
+            const int pos = a.position + step;
+            const bool last_step = (step == a.n_steps - 1);
+            int i_dn = 0, i_fa = 0;
+
+            for (int layer = 0; layer < n_layers; ++layer) {
+                const LayerRec& L = s.layers[layer];
+                const unsigned ep = epoch_of(a, step, layer);
+                const bool dn = (L.type == 0);
+                const bf16* w_post = (const bf16*)(dn ? L.p[DN_POST_NORM] : L.p[FA_POST_NORM]);
+
+                // ---- DeltaNet: issue the state / conv loads of stage B before any waiting ----
+                const int pp0 = part_begin(DN_V_SIZE / 2, b, G), pp1 = part_begin(DN_V_SIZE / 2, b + 1, G);   // value-row pairs
+                float4 st0 = make_float4(0, 0, 0, 0), st1 = st0, cv0 = st0, cv1 = st0;
+                float* conv = a.conv_bufs + (size_t)i_dn * DN_CONV_CH * 4;
+                float* state = a.dn_states + (size_t)i_dn * DN_HEADS * DN_V * DN_K;
+                const int my_pair = pp0 + warp;                     // at most one pair per warp when G >= 64
+                if (dn && my_pair < pp1) {
+                    const int r0 = 2 * my_pair;                     // rows r0, r0+1 of head r0 >> 7
+                    st0 = ld_cg(reinterpret_cast<const float4*>(state + (size_t)r0 * DN_K) + lane);
+                    st1 = ld_cg(reinterpret_cast<const float4*>(state + (size_t)(r0 + 1) * DN_K) + lane);
+                    cv0 = ld_cg(reinterpret_cast<const float4*>(conv) + 2 * DN_QK_SIZE + r0);
+                    cv1 = ld_cg(reinterpret_cast<const float4*>(conv) + 2 * DN_QK_SIZE + r0 + 1);
+                }
+
+                // ================= stage A: input norm + fused projection =================
+                {
+                    uint32_t raw;
+                    if (layer == 0) raw = __ldg(reinterpret_cast<const uint32_t*>(a.embed + (size_t)tok * HIDDEN) + tid);
+                    else if (a.dbg_teacher) raw = __ldg(reinterpret_cast<const uint32_t*>(a.dbg_teacher + layer * HIDDEN) + tid);
+                    else raw = poll_word(&ws->h2[tid], epoch_of(a, step, layer - 1), ab);
+                    reinterpret_cast<uint32_t*>(s.h)[tid] = raw;
+                    rmsnorm_pair(raw, (const bf16*)L.p[0], s.x, s.red);
+                    cons_sync();
+                    const int ntl = dn ? TILES_A_DN : TILES_A_FA;
+                    const int u0 = part_begin(ntl, b, G), u1 = part_begin(ntl, b + 1, G);
+                    consume_k1024<1>(ring, u1 - u0, s.x, ab, [&](int row, const float (*acc)[2]) {
+                        st_word(&ws->xa[(u0 * 8 + row) >> 1], pack_bf16x2(acc[0][0], acc[0][1]), ep);
+                    });
+                }
+
+                if (dn) {
+                    // ================= stage B (DeltaNet): conv, norms, recurrence =================
+                    const bf16* conv_w = (const bf16*)L.p[DN_CONV];
+                    const int hlo = (2 * pp0) >> 7, hhi = (pp1 > pp0) ? ((2 * pp1 - 1) >> 7) : hlo;   // at most two heads per CTA
+                    {
+                        // 256 threads: slot (head) x {q,k} x 64 words of two channels
+                        const int slot = tid >> 7, isk = (tid >> 6) & 1, wi = tid & 63;
+                        const bool act = tid < 256 && (pp1 > pp0) && (hlo + slot <= hhi);
+                        float c0 = 0.f, c1 = 0.f, sq = 0.f;
+                        if (act) {
+                            const int ch = isk * DN_QK_SIZE + (hlo + slot) * DN_K + 2 * wi;
+                            const float4 s0 = ld_cg(reinterpret_cast<const float4*>(conv) + ch);
+                            const float4 s1 = ld_cg(reinterpret_cast<const float4*>(conv) + ch + 1);
+                            const uint32_t xw = poll_word(&ws->xa[ch >> 1], ep, ab);
+                            c0 = conv_silu(conv_w, ch, s0, bf_lo(xw));
+                            c1 = conv_silu(conv_w, ch + 1, s1, bf_hi(xw));
+                            sq = rbf(c0 * c0) + rbf(c1 * c1);
+                        }
+                        const float wsum = warp_sum(sq);
+                        cons_sync();
+                        if (lane == 0) s.red[warp] = wsum;
+                        cons_sync();
+                        if (act) {
+                            float tot = s.red[warp & ~1] + s.red[warp | 1];
+                            tot = rbf(tot);
+                            tot = rbf(tot + 1e-6f);
+                            // torch's CPU rsqrt on a 16-element bf16 tensor takes the scalar path, which rounds
+                            // sqrt to bf16 before the reciprocal; decode mirrors that.
+                            const float inv = rbf(1.0f / rbf(sqrtf(tot)));
+                            float n0 = rbf(c0 * inv), n1 = rbf(c1 * inv);
+                            if (!isk) { n0 *= 0.08838834764831845f; n1 *= 0.08838834764831845f; }   // q * 1/sqrt(128) in f32
+                            s.qk[slot][isk][2 * wi] = n0;
+                            s.qk[slot][isk][2 * wi + 1] = n1;
+                        }
+                        if (tid >= 256 && tid < 258 && (pp1 > pp0) && hlo + (tid - 256) <= hhi) {
+                            const int sl = tid - 256, h = hlo + sl;
+                            const uint32_t bw = poll_word(&ws->xa[(DN_CONV_CH + DN_V_SIZE + h) >> 1], ep, ab);
+                            const uint32_t aw = poll_word(&ws->xa[(DN_CONV_CH + DN_V_SIZE + DN_HEADS + h) >> 1], ep, ab);
+                            const float bb = (h & 1) ? bf_hi(bw) : bf_lo(bw);
+                            const float aa = (h & 1) ? bf_hi(aw) : bf_lo(aw);
+                            const float x = aa + bf2f(((const bf16*)L.p[DN_DTBIAS])[h]);
+                            const float sp = (x > 20.f) ? x : log1pf(expf(x));
+                            const float g = -expf(bf2f(((const bf16*)L.p[DN_ALOG])[h])) * sp;
+                            s.hd[sl][0] = rbf(sigmoid_f(bb));
+                            s.hd[sl][1] = expf(g);
+                        }
+                        cons_sync();
+                    }
+                    if (my_pair < pp1) {
+                        const int r0 = 2 * my_pair, h = r0 >> 7, slot = h - hlo;
+                        const float4 q4 = *reinterpret_cast<const float4*>(&s.qk[slot][0][lane * 4]);
+                        const float4 k4 = *reinterpret_cast<const float4*>(&s.qk[slot][1][lane * 4]);
+                        const float beta = s.hd[slot][0], decay = s.hd[slot][1];
+                        const int ch = 2 * DN_QK_SIZE + r0;
+                        const uint32_t vw = poll_word(&ws->xa[ch >> 1], ep, ab);
+                        const float vv[2] = {conv_silu(conv_w, ch, cv0, bf_lo(vw)), conv_silu(conv_w, ch + 1, cv1, bf_hi(vw))};
+                        float4 sv[2] = {st0, st1};
+                        float ov[2];
+#pragma unroll
+                        for (int r = 0; r < 2; ++r) {
+                            float4 t = sv[r];
+                            t.x = __fmul_rn(t.x, decay); t.y = __fmul_rn(t.y, decay); t.z = __fmul_rn(t.z, decay); t.w = __fmul_rn(t.w, decay);
+                            float kv = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(t.x, k4.x), __fmul_rn(t.y, k4.y)), __fmul_rn(t.z, k4.z)), __fmul_rn(t.w, k4.w));
+                            kv = warp_sum(kv);
+                            const float delta = __fmul_rn(__fsub_rn(vv[r], kv), beta);
+                            t.x = __fadd_rn(t.x, __fmul_rn(k4.x, delta)); t.y = __fadd_rn(t.y, __fmul_rn(k4.y, delta));
+                            t.z = __fadd_rn(t.z, __fmul_rn(k4.z, delta)); t.w = __fadd_rn(t.w, __fmul_rn(k4.w, delta));
+                            float o = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(t.x, q4.x), __fmul_rn(t.y, q4.y)), __fmul_rn(t.z, q4.z)), __fmul_rn(t.w, q4.w));
+                            ov[r] = warp_sum(o);
+                            reinterpret_cast<float4*>(state + (size_t)(r0 + r) * DN_K)[lane] = t;
+                        }
+                        if (lane == 0) st_word(&ws->o[my_pair], pack_bf16x2(ov[0], ov[1]), ep);
+                    }
+
+                    // ================= stage C (DeltaNet): gated norm (one head per warp), conv shift =================
+                    {
+                        const int h = warp;
+                        uint32_t o0, o1, z0, z1;
+                        poll2(&ws->o[h * 64 + lane * 2], &ws->o[h * 64 + lane * 2 + 1], ep, ab, o0, o1);
+                        poll2(&ws->xa[(DN_CONV_CH >> 1) + h * 64 + lane * 2], &ws->xa[(DN_CONV_CH >> 1) + h * 64 + lane * 2 + 1], ep, ab, z0, z1);
+                        const uint2 nrw = __ldg(reinterpret_cast<const uint2*>(L.p[DN_NORM]) + lane);
+                        const float ov[4] = {bf_lo(o0), bf_hi(o0), bf_lo(o1), bf_hi(o1)};
+                        const float zv[4] = {bf_lo(z0), bf_hi(z0), bf_lo(z1), bf_hi(z1)};
+                        const float nw[4] = {bf_lo(nrw.x), bf_hi(nrw.x), bf_lo(nrw.y), bf_hi(nrw.y)};
+                        const float var = warp_sum(ov[0] * ov[0] + ov[1] * ov[1] + ov[2] * ov[2] + ov[3] * ov[3]) * (1.0f / DN_V);
+                        const float r = rsqrt_ieee(var + RMS_EPS);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const float n = rbf(ov[i] * r);
+                            const float t = rbf(nw[i] * n);
+                            s.x[h * DN_V + lane * 4 + i] = f2bf(t * silu_f(zv[i]));
+                        }
+                    }
+                    ++i_dn;
+                } else {
+                    // ================= attention: B1 scores, B2 P.V partials, B3 merge + gate =================
+                    bf16* kc = a.k_cache + (size_t)i_fa * FA_KV_HEADS * a.max_seq_len * FA_HEAD_DIM;
+                    bf16* vc = a.v_cache + (size_t)i_fa * FA_KV_HEADS * a.max_seq_len * FA_HEAD_DIM;
+                    const int Lc = pos + 1;
+                    int nchunk = (Lc + 31) / 32; if (nchunk > ATT_MAX_CHUNKS) nchunk = ATT_MAX_CHUNKS;
+                    const int clen = (Lc + nchunk - 1) / nchunk;
+                    const bool att_cta = b < FA_KV_HEADS * nchunk;
+                    const int kvh = b / nchunk, chunk = b % nchunk;
+                    const int j0 = chunk * clen, j1 = min(Lc, j0 + clen);
+                    if (att_cta) {
+                        if (warp < FA_GQA + 1) {
+                            // warps 0..3: the four query heads of this kv head; warp 4: the new key.
+                            // lane l holds elements {2l, 2l+1} + 64*i, i = 0..3 (four flagged words)
+                            const bool isq = warp < FA_GQA;
+                            const int e0 = isq ? (kvh * FA_GQA + warp) * 2 * FA_HEAD_DIM : FA_QPROJ + kvh * FA_HEAD_DIM;
+                            const bf16* nw = (const bf16*)(isq ? L.p[FA_QNORM] : L.p[FA_KNORM]);
+                            float xv[8], ss = 0.f;
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const uint32_t wv = poll_word(&ws->xa[(e0 >> 1) + lane + 32 * i], ep, ab);
+                                xv[2 * i] = bf_lo(wv); xv[2 * i + 1] = bf_hi(wv);
+                                ss += xv[2 * i] * xv[2 * i] + xv[2 * i + 1] * xv[2 * i + 1];
+                            }
+                            const float r = rsqrt_ieee(warp_sum(ss) * (1.0f / FA_HEAD_DIM) + RMS_EPS);
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const int d = 2 * lane + 64 * i;
+                                xv[2 * i] = rbf((xv[2 * i] * r) * (1.0f + bf2f(nw[d])));
+                                xv[2 * i + 1] = rbf((xv[2 * i + 1] * r) * (1.0f + bf2f(nw[d + 1])));
+                            }
+                            // RoPE on dims [0,64): pairs (d, d+32).  Lanes 0-15 hold dims 2l,2l+1; lanes 16-31 hold 32+2(l-16), +1.
+                            {
+                                const int fi = 2 * (lane & 15);
+                                const float ang0 = (float)pos * c_rope_inv_freq[fi], ang1 = (float)pos * c_rope_inv_freq[fi + 1];
+                                const float c0 = rbf(cosf(ang0)), s0 = rbf(sinf(ang0)), c1 = rbf(cosf(ang1)), s1 = rbf(sinf(ang1));
+                                const float p0 = __shfl_xor_sync(0xffffffffu, xv[0], 16), p1 = __shfl_xor_sync(0xffffffffu, xv[1], 16);
+                                if (lane < 16) {   // own = x1, partner = x2
+                                    xv[0] = rbf(rbf(xv[0] * c0) + rbf(-p0 * s0));
+                                    xv[1] = rbf(rbf(xv[1] * c1) + rbf(-p1 * s1));
+                                } else {           // own = x2, partner = x1
+                                    xv[0] = rbf(rbf(xv[0] * c0) + rbf(p0 * s0));
+                                    xv[1] = rbf(rbf(xv[1] * c1) + rbf(p1 * s1));
+                                }
+                            }
+                            float* dst = isq ? s.q[warp] : s.kcur;
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) { dst[2 * lane + 64 * i] = xv[2 * i]; dst[2 * lane + 64 * i + 1] = xv[2 * i + 1]; }
+                            if (!isq && pos >= j0 && pos < j1) {
+                                uint32_t* krow = reinterpret_cast<uint32_t*>(kc + ((size_t)kvh * a.max_seq_len + pos) * FA_HEAD_DIM);
+#pragma unroll
+                                for (int i = 0; i < 4; ++i) krow[lane + 32 * i] = pack_bf16x2(xv[2 * i], xv[2 * i + 1]);
+                                __threadfence();
+                            }
+                        } else if (warp == FA_GQA + 1 && pos >= j0 && pos < j1) {
+                            uint32_t* vrow = reinterpret_cast<uint32_t*>(vc + ((size_t)kvh * a.max_seq_len + pos) * FA_HEAD_DIM);
+#pragma unroll
+                            for (int i = 0; i < 4; ++i)
+                                vrow[lane + 32 * i] = poll_word(&ws->xa[((FA_QPROJ + FA_KV_SIZE + kvh * FA_HEAD_DIM) >> 1) + lane + 32 * i], ep, ab);
+                            __threadfence();
+                        }
+                        cons_sync();
+                        float qr[FA_GQA][8];
+#pragma unroll
+                        for (int g = 0; g < FA_GQA; ++g)
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) qr[g][i] = s.q[g][lane * 8 + i];
+                        for (int j = j0 + warp; j < j1; j += NCONS_WARPS) {
+                            float kf[8];
+                            if (j == pos) {
+#pragma unroll
+                                for (int i = 0; i < 8; ++i) kf[i] = s.kcur[lane * 8 + i];
+                            } else {
+                                unpack8(ld_cg(reinterpret_cast<const uint4*>(kc + ((size_t)kvh * a.max_seq_len + j) * FA_HEAD_DIM) + lane), kf);
+                            }
+#pragma unroll
+                            for (int g = 0; g < FA_GQA; ++g) {
+                                float d = 0.f;
+#pragma unroll
+                                for (int i = 0; i < 8; ++i) d = fmaf(qr[g][i], kf[i], d);
+                                d = warp_sum(d);
+                                if (lane == 0) st_word(&ws->sc[kvh * FA_GQA + g][j], __float_as_uint(rbf(d) * 0.0625f), ep);
+                            }
+                        }
+                        // ---- B2: softmax statistics over the whole context, then P.V over this chunk ----
+                        if (warp < FA_GQA) {
+                            const u64* sc = ws->sc[kvh * FA_GQA + warp];
+                            float mx = -INFINITY;
+                            for (int j = lane; j < Lc; j += 32) mx = fmaxf(mx, __uint_as_float(poll_word(sc + j, ep, ab)));
+                            mx = warp_max(mx);
+                            float sm = 0.f;
+                            for (int j = lane; j < Lc; j += 32) sm += expf(__uint_as_float((uint32_t)ld_word(sc + j)) - mx);
+                            sm = warp_sum(sm);
+                            if (lane == 0) { s.ml[warp][0] = mx; s.ml[warp][1] = sm; }
+                        }
+                        cons_sync();
+                        const int g = tid >> 7, d2 = tid & 127;       // 4 heads x 128 threads, 2 dims each
+                        float acc0 = 0.f, acc1 = 0.f;
+                        for (int t0 = j0; t0 < j1; t0 += 256) {
+                            const int tn = min(256, j1 - t0);
+                            cons_sync();
+                            for (int i = tid; i < FA_GQA * tn; i += NCONS) {
+                                const int gg = i / tn, jj = i % tn;
+                                const float sv = __uint_as_float((uint32_t)ld_word(&ws->sc[kvh * FA_GQA + gg][t0 + jj]));
+                                s.p[gg][jj] = rbf(expf(sv - s.ml[gg][0]) / s.ml[gg][1]);
+                            }
+                            cons_sync();
+                            const uint32_t* vb = reinterpret_cast<const uint32_t*>(vc + ((size_t)kvh * a.max_seq_len + t0) * FA_HEAD_DIM) + d2;
+#pragma unroll 4
+                            for (int jj = 0; jj < tn; ++jj) {
+                                const uint32_t vr = ld_cg(vb + (size_t)jj * (FA_HEAD_DIM / 2));
+                                const float p = s.p[g][jj];
+                                acc0 = fmaf(p, bf_lo(vr), acc0);
+                                acc1 = fmaf(p, bf_hi(vr), acc1);
+                            }
+                        }
+                        reinterpret_cast<float2*>(ws->att_part[chunk][kvh * FA_GQA + g])[d2] = make_float2(acc0, acc1);
+                        __threadfence();
+                        cons_sync();
+                        if (tid == 0) st_release(&ws->att_flag[kvh][chunk], ep);
+                    }
+                    // ---- B3: CTA h < 8 merges the partials of query head h and applies the sigmoid gate ----
+                    if (b < FA_Q_HEADS) {
+                        const int qh = b;
+                        if (tid < nchunk) {
+                            unsigned it = 0;
+                            while (ld_acquire(&ws->att_flag[qh / FA_GQA][tid]) != ep && !ab.on()) {
+                                if (++it > POLL_LIMIT) { ab.raise(ERR_BARRIER_TIMEOUT); break; }
+                            }
+                        }
+                        cons_sync();
+                        if (tid < 64) {
+                            const int d = tid * 4;
+                            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                            for (int c = 0; c < nchunk; ++c) {
+                                const float4 pv = ld_cg(reinterpret_cast<const float4*>(&ws->att_part[c][qh][d]));
+                                acc.x += pv.x; acc.y += pv.y; acc.z += pv.z; acc.w += pv.w;
+                            }
+                            uint32_t g0, g1;
+                            const int ge = qh * 2 * FA_HEAD_DIM + FA_HEAD_DIM + d;
+                            poll2(&ws->xa[ge >> 1], &ws->xa[(ge >> 1) + 1], ep, ab, g0, g1);
+                            const float u0 = rbf(acc.x) * rbf(sigmoid_f(bf_lo(g0))), u1 = rbf(acc.y) * rbf(sigmoid_f(bf_hi(g0)));
+                            const float u2 = rbf(acc.z) * rbf(sigmoid_f(bf_lo(g1))), u3 = rbf(acc.w) * rbf(sigmoid_f(bf_hi(g1)));
+                            st_word(&ws->o[(qh * FA_HEAD_DIM + d) >> 1], pack_bf16x2(u0, u1), ep);
+                            st_word(&ws->o[((qh * FA_HEAD_DIM + d) >> 1) + 1], pack_bf16x2(u2, u3), ep);
+                        }
+                    }
+                    // ---- stage C (attention): the gated attention output is the GEMV input ----
+                    {
+                        uint32_t w0, w1;
+                        poll2(&ws->o[tid], &ws->o[tid + NCONS], ep, ab, w0, w1);
+                        reinterpret_cast<uint32_t*>(s.x)[tid] = w0;
+                        reinterpret_cast<uint32_t*>(s.x)[tid + NCONS] = w1;
+                    }
+                    ++i_fa;
+                }
+                cons_sync();
+                if (dn) {
+                    // this CTA has now seen all of `o`: every CTA finished stage B and nobody reads the
+                    // old conv window of this layer any more -> shift in this token's inputs
+                    for (int c = part_begin(DN_CONV_CH / 2, b, G) + tid; c < part_begin(DN_CONV_CH / 2, b + 1, G); c += NCONS) {
+                        const uint32_t xw = poll_word(&ws->xa[c], ep, ab);
+                        const float4 c0 = ld_cg(reinterpret_cast<const float4*>(conv) + 2 * c);
+                        const float4 c1 = ld_cg(reinterpret_cast<const float4*>(conv) + 2 * c + 1);
+                        reinterpret_cast<float4*>(conv)[2 * c] = make_float4(c0.y, c0.z, c0.w, bf_lo(xw));
+                        reinterpret_cast<float4*>(conv)[2 * c + 1] = make_float4(c1.y, c1.z, c1.w, bf_hi(xw));
+                        __threadfence();
+                    }
+                }
+
+                // ---- stage C tail: output projection (K = 2048, 4 rows per tile) + residual ----
+                {
+                    const bf16* hin = s.h;
+                    const int u0 = part_begin(TILES_C, b, G), nt = part_begin(TILES_C, b + 1, G) - u0;
+                    float x[16];
+                    unpack8(*reinterpret_cast<const uint4*>(s.x + (warp & 3) * 512 + lane * 8), x);
+                    unpack8(*reinterpret_cast<const uint4*>(s.x + (warp & 3) * 512 + (32 + lane) * 8), x + 8);
+                    for (int ti = 0; ti < nt; ++ti) {
+                        const unsigned tile = ring.t + (unsigned)ti;
+                        mbar_wait(ring.full_bar(tile), ring.phase(tile), ab);
+                        const uint32_t base = ring.slot_addr(tile) + (uint32_t)(warp >> 2) * 4096u + (uint32_t)(warp & 3) * 1024u + (uint32_t)lane * 16u;
+                        const uint4 q0 = lds128(base), q1 = lds128(base + 512);
+                        const float acc = warp_sum(dot8(q1, x + 8, dot8(q0, x, 0.f)));
+                        if (lane == 0) { s.part[ti * 16 + warp] = acc; mbar_arrive(ring.empty_bar(tile), 1); }
+                    }
+                    ring.t += (unsigned)nt;
+                    cons_sync();
+                    if (tid < nt * 2) {
+                        const int ti = tid >> 1, pr = tid & 1;
+                        const float* pp = &s.part[ti * 16 + pr * 8];
+                        const float y0 = ((pp[0] + pp[1]) + pp[2]) + pp[3], y1 = ((pp[4] + pp[5]) + pp[6]) + pp[7];
+                        const int row = (u0 + ti) * 4 + 2 * pr;
+                        st_word(&ws->h1[row >> 1], pack_bf16x2(bf2f(hin[row]) + rbf(y0), bf2f(hin[row + 1]) + rbf(y1)), ep);
+                    }
+                }
+
+                // ================= stage D: post norm, gate/up with SiLU*up =================
+                {
+                    const uint32_t raw = poll_word(&ws->h1[tid], ep, ab);
+                    reinterpret_cast<uint32_t*>(s.h1)[tid] = raw;
+                    rmsnorm_pair(raw, w_post, s.x, s.red);
+                    cons_sync();
+                    const int u0 = part_begin(UNITS_D, b, G), u1 = part_begin(UNITS_D, b + 1, G);
+                    consume_k1024<2>(ring, u1 - u0, s.x, ab, [&](int row, const float (*acc)[2]) {
+                        const float m0 = rbf(silu_f(rbf(acc[0][0]))) * rbf(acc[1][0]);
+                        const float m1 = rbf(silu_f(rbf(acc[0][1]))) * rbf(acc[1][1]);
+                        st_word(&ws->m[(u0 * 8 + row) >> 1], pack_bf16x2(m0, m1), ep);
+                    });
+                }
+
+                // ================= stage E: down projection (K = 3584, 2 rows per tile) + residual =================
+                {
+                    for (int i = tid; i < INTER / 2; i += NCONS) reinterpret_cast<uint32_t*>(s.x)[i] = poll_word(&ws->m[i], ep, ab);
+                    cons_sync();
+                    const int u0 = part_begin(TILES_E, b, G), nt = part_begin(TILES_E, b + 1, G) - u0;
+                    uint4 xp[7];
+#pragma unroll
+                    for (int j = 0; j < 7; ++j) xp[j] = *reinterpret_cast<const uint4*>(s.x + (warp & 1) * 1792 + (j * 32 + lane) * 8);
+                    for (int g = 0; g < nt; g += 4) {
+                        const int ti = g + (warp >> 2);
+                        if (ti < nt) {
+                            const unsigned tile = ring.t + (unsigned)ti;
+                            mbar_wait(ring.full_bar(tile), ring.phase(tile), ab);
+                            const uint32_t base = ring.slot_addr(tile) + (uint32_t)((warp & 3) >> 1) * 7168u + (uint32_t)(warp & 1) * 3584u + (uint32_t)lane * 16u;
+                            float acc = 0.f;
+#pragma unroll
+                            for (int j = 0; j < 7; ++j) acc = dot8p(lds128(base + j * 512), xp[j], acc);
+                            acc = warp_sum(acc);
+                            if (lane == 0) { s.part[ti * 4 + (warp & 3)] = acc; mbar_arrive(ring.empty_bar(tile), 4); }
+                        }
+                    }
+                    ring.t += (unsigned)nt;
+                    cons_sync();
+                    if (tid < nt) {
+                        const float y0 = s.part[tid * 4] + s.part[tid * 4 + 1], y1 = s.part[tid * 4 + 2] + s.part[tid * 4 + 3];
+                        const int row = (u0 + tid) * 2;
+                        const uint32_t hv = pack_bf16x2(bf2f(s.h1[row]) + rbf(y0), bf2f(s.h1[row + 1]) + rbf(y1));
+                        st_word(&ws->h2[row >> 1], hv, ep);
+                        if (last_step && a.dbg_hidden) reinterpret_cast<uint32_t*>(a.dbg_hidden + layer * HIDDEN)[row >> 1] = hv;
+                        if (last_step && layer == n_layers - 1 && a.hidden_out) reinterpret_cast<uint32_t*>(a.hidden_out)[row >> 1] = hv;
+                    }
+                }
+            }
+
+            // ================= LM head: final norm, 248320 x 1024 GEMV, arg-max =================
+            if (!a.lm_last_only || last_step) {
+                const unsigned ep_lm = epoch_of(a, step, 24);
+                const uint32_t raw = poll_word(&ws->h2[tid], epoch_of(a, step, n_layers - 1), ab);
+                rmsnorm_pair(raw, a.final_norm, s.x, s.red);
+                cons_sync();
+                float best = -INFINITY;
+                int best_i = 0x7fffffff;
+                float* lg = (last_step ? a.logits_out : nullptr);
+                const int u0 = part_begin(TILES_LM, b, G), u1 = part_begin(TILES_LM, b + 1, G);
+                consume_k1024<1>(ring, u1 - u0, s.x, ab, [&](int row, const float (*acc)[2]) {
+                    const int r0 = u0 * 8 + row;
+                    const float v0 = rbf(acc[0][0]), v1 = rbf(acc[0][1]);
+                    if (lg) { lg[r0] = v0; lg[r0 + 1] = v1; }
+                    if (v0 > best) { best = v0; best_i = r0; }
+                    if (v1 > best) { best = v1; best_i = r0 + 1; }
+                });
+                // lane 0 of every warp holds that warp's best (rows ascend within a warp)
+                cons_sync();
+                if (lane == 0) { s.part[warp] = best; reinterpret_cast<int*>(s.part)[NCONS_WARPS + warp] = best_i; }
+                cons_sync();
+                if (tid == 0) {
+                    float bv = s.part[0]; int bi = reinterpret_cast<int*>(s.part)[NCONS_WARPS];
+                    for (int w = 1; w < NCONS_WARPS; ++w) {
+                        const float v = s.part[w]; const int i = reinterpret_cast<int*>(s.part)[NCONS_WARPS + w];
+                        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+                    }
+                    st_word(&ws->lm[0][b], __float_as_uint(bv), ep_lm);
+                    st_word(&ws->lm[1][b], (uint32_t)bi, ep_lm);
+                }
+                if (warp == 0) {
+                    float bv = -INFINITY; int bi = 0x7fffffff;
+                    for (int c = lane; c < G; c += 32) {
+                        const float v = __uint_as_float(poll_word(&ws->lm[0][c], ep_lm, ab));
+                        const int i = (int)poll_word(&ws->lm[1][c], ep_lm, ab);
+                        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        const float v = __shfl_xor_sync(0xffffffffu, bv, o); const int i = __shfl_xor_sync(0xffffffffu, bi, o);
+                        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+                    }
+                    if (lane == 0) s.tok = bi;
+                }
+                cons_sync();
+                tok = s.tok;
+                if (b == 0 && tid == 0) {
+                    if (a.out_tokens) a.out_tokens[step] = tok;
+                    if (last_step && a.out_token) *a.out_token = tok;
+                }
+            }
+        }
+    }
+    __syncthreads();   // the producer has drained its copies; nothing is in flight when the CTA exits
+}
+
+}  // namespace q35
+
+// ======================================= host side ==========================================
+#include <cmath>
+#include <cstdlib>
+#include <mutex>
+
+#include "runtime.h"
+
+namespace q35 {
+
+static void rope_table(float* t) {
+    for (int i = 0; i < FA_ROT / 2; ++i) {
+        const float e = (float)(2 * i) / (float)FA_ROT;
+        const float p = (float)std::pow(1.0e7, (double)e);
+        t[i] = 1.0f / p;
+    }
+}
+
+static int decode_grid() {
+    // one persistent CTA per SM; MEGAKERNEL_DECODE_BLOCKS overrides (same knob as the reference, kernel.cu:926-943)
+    int g = device_sm_count();
+    if (const char* s = getenv("MEGAKERNEL_DECODE_BLOCKS")) {
+        const int v = atoi(s);
+        if (v >= 64 && v <= g) g = v;
+    }
+    return g;
+}
+
+static unsigned g_epoch[64] = {};
+
+static int launch_decode_impl(const DecodeArgs& in, cudaStream_t stream) {
+    static std::once_flag once[64];
+    static bool ready[64] = {};
+    int dev = 0;
+    Q35_CUDA_OK(cudaGetDevice(&dev));
+    dev &= 63;
+    std::call_once(once[dev], [&] {
+        float t[FA_ROT / 2];
+        rope_table(t);
+        int nb = 0;
+        if (cudaMemcpyToSymbol(c_rope_inv_freq, t, sizeof(t)) == cudaSuccess &&
+            cudaFuncSetAttribute(decode_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem)) == cudaSuccess &&
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, decode_stream_kernel, STREAM_THREADS, sizeof(Smem)) == cudaSuccess && nb >= 1)
+            ready[dev] = true;
+    });
+    if (!ready[dev]) { set_error("decode kernel cannot be made resident on this device (needs %zu bytes of shared memory)", sizeof(Smem)); return QWEN35_ERR_CUDA; }
+
+    DecodeArgs a = in;
+    if (a.n_steps <= 0) return QWEN35_OK;
+    if (!a.layers || !a.embed || !a.final_norm || !a.lm_head || !a.k_cache || !a.v_cache || !a.dn_states || !a.conv_bufs) {
+        set_error("null tensor pointer");
+        return QWEN35_ERR_BAD_ARG;
+    }
+    if (a.position < 0 || a.max_seq_len <= 0 || a.position + a.n_steps > a.max_seq_len || a.max_seq_len > MAX_CTX) {
+        set_error("position %d + %d steps exceeds max_seq_len %d (library limit %d)", a.position, a.n_steps, a.max_seq_len, MAX_CTX);
+        return QWEN35_ERR_BAD_ARG;
+    }
+    if (!a.token_in && !a.forced_ids && (a.token_imm < 0 || a.token_imm >= VOCAB)) {
+        set_error("token id %d out of range", a.token_imm);
+        return QWEN35_ERR_BAD_ARG;
+    }
+    if (device_sm_count() < 64) { set_error("needs at least 64 SMs"); return QWEN35_ERR_UNSUPPORTED; }
+    a.ws = (StreamWorkspace*)get_workspace();
+    if (!a.ws) return QWEN35_ERR_CUDA;
+    // epochs tag every flagged word; they only ever grow.  On wrap-around the words are cleared.
+    const unsigned long long need = 32ull * (unsigned long long)a.n_steps + 64ull;
+    if ((unsigned long long)g_epoch[dev] + need >= 0xffffff00ull) {
+        Q35_CUDA_OK(cudaMemsetAsync((char*)a.ws + 256, 0, sizeof(StreamWorkspace) - 256, stream));
+        g_epoch[dev] = 0;
+    }
+    a.epoch_base = g_epoch[dev];
+    g_epoch[dev] += (unsigned)(32u * (unsigned)a.n_steps);
+    void* params[] = {(void*)&a};
+    Q35_CUDA_OK(cudaLaunchCooperativeKernel((const void*)decode_stream_kernel, dim3(decode_grid()), dim3(STREAM_THREADS), params, sizeof(Smem), stream));
+    g_launches.fetch_add(1);
+    return QWEN35_OK;
+}
+
+size_t workspace_bytes() { return sizeof(StreamWorkspace); }
+
+}  // namespace q35
+
+extern "C" int launch_decode(
+    int input_token_id, int* output_token_id,
+    const void* embed_weight, const LayerWeights* layer_weights,
+    const void* final_norm_weight, const void* lm_head_weight,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* hidden_buffer, void*, void*, void*, void*, void*, void*, void*, void*, void*, void*,
+    unsigned int*, unsigned int*, float*, int*, unsigned int*,
+    int position, int max_seq_len, qwen35_stream_t stream) {
+    q35::DecodeArgs a = {};
+    a.layers = reinterpret_cast<const q35::LayerRec*>(layer_weights);
+    a.embed = (const q35::bf16*)embed_weight;
+    a.final_norm = (const q35::bf16*)final_norm_weight;
+    a.lm_head = (const q35::bf16*)lm_head_weight;
+    a.k_cache = (q35::bf16*)fa_k_cache;
+    a.v_cache = (q35::bf16*)fa_v_cache;
+    a.dn_states = (float*)dn_states;
+    a.conv_bufs = (float*)conv_bufs;
+    a.token_imm = input_token_id;
+    a.out_token = output_token_id;
+    a.hidden_out = (q35::bf16*)hidden_buffer;
+    a.position = position;
+    a.max_seq_len = max_seq_len;
+    a.n_steps = 1;
+    return q35::launch_decode_impl(a, (cudaStream_t)stream);
+}
+
+extern "C" int qwen35_b200_decode_steps(const Qwen35DecodeArgs* in, qwen35_stream_t stream) {
+    if (!in) { q35::set_error("null args"); return QWEN35_ERR_BAD_ARG; }
+    q35::DecodeArgs a = {};
+    a.layers = reinterpret_cast<const q35::LayerRec*>(in->layer_weights);
+    a.embed = (const q35::bf16*)in->embed_weight;
+    a.final_norm = (const q35::bf16*)in->final_norm_weight;
+    a.lm_head = (const q35::bf16*)in->lm_head_weight;
+    a.k_cache = (q35::bf16*)in->fa_k_cache;
+    a.v_cache = (q35::bf16*)in->fa_v_cache;
+    a.dn_states = (float*)in->dn_states;
+    a.conv_bufs = (float*)in->conv_bufs;
+    a.token_in = in->token_in;
+    a.token_imm = in->token_imm;
+    a.forced_ids = in->forced_ids;
+    a.out_token = in->out_token;
+    a.out_tokens = in->out_tokens;
+    a.logits_out = in->logits_out;
+    a.hidden_out = (q35::bf16*)in->hidden_out;
+    a.dbg_hidden = (q35::bf16*)in->dbg_hidden;
+    a.dbg_teacher = (const q35::bf16*)in->dbg_teacher;
+    a.position = in->position;
+    a.max_seq_len = in->max_seq_len;
+    a.n_steps = in->n_steps;
+    a.lm_last_only = in->lm_last_only;
+    a.dbg_num_layers = in->dbg_num_layers;
+    return q35::launch_decode_impl(a, (cudaStream_t)stream);
+}
+
+// Debug: synchronise the device and decode one flagged-word vector of the workspace to bf16 on the host.
+// which: 0 = xa (8224), 1 = o (2048), 2 = h1 (1024), 3 = m (3584), 4 = h2 (1024)
+extern "C" int qwen35_b200_debug_read(int which, void* host_out) {
+    using namespace q35;
+    StreamWorkspace* ws = (StreamWorkspace*)get_workspace();
+    if (!ws || !host_out) return QWEN35_ERR_BAD_ARG;
+    const u64* src; int n;
+    switch (which) {
+        case 0: src = ws->xa; n = DN_PROJ_ROWS / 2; break;
+        case 1: src = ws->o; n = DN_V_SIZE / 2; break;
+        case 2: src = ws->h1; n = HIDDEN / 2; break;
+        case 3: src = ws->m; n = INTER / 2; break;
+        case 4: src = ws->h2; n = HIDDEN / 2; break;
+        default: return QWEN35_ERR_BAD_ARG;
+    }
+    static u64 tmp[DN_PROJ_ROWS / 2];
+    Q35_CUDA_OK(cudaDeviceSynchronize());
+    Q35_CUDA_OK(cudaMemcpy(tmp, src, (size_t)n * 8, cudaMemcpyDeviceToHost));
+    for (int i = 0; i < n; ++i) ((uint32_t*)host_out)[i] = (uint32_t)tmp[i];
+    return QWEN35_OK;
+}
+
+extern "C" int qwen35_b200_rope_inv_freq(float* host_out32) {
+    if (!host_out32) return QWEN35_ERR_BAD_ARG;
+    q35::rope_table(host_out32);
+    return QWEN35_OK;
+}

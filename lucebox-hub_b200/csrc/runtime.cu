@@ -5,12 +5,11 @@
 #include <cstdio>
 #include <mutex>
 
-#include "decode_bf16.cuh"
 
 namespace q35 {
 
 static constexpr int MAX_DEVICES = 64;
-static Workspace* g_ws[MAX_DEVICES] = {};
+static void* g_ws[MAX_DEVICES] = {};
 static int g_sms[MAX_DEVICES] = {};
 static std::mutex g_mu;
 static thread_local char g_err[512] = "";
@@ -23,7 +22,7 @@ void set_error(const char* fmt, ...) {
     va_end(ap);
 }
 
-Workspace* get_workspace() {
+void* get_workspace() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) {
         set_error("no current CUDA device");
@@ -31,9 +30,9 @@ Workspace* get_workspace() {
     }
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g_ws[dev]) {
-        Workspace* p = nullptr;
-        cudaError_t e = cudaMalloc(&p, sizeof(Workspace));
-        if (e == cudaSuccess) e = cudaMemset(p, 0, sizeof(Workspace));
+        void* p = nullptr;
+        cudaError_t e = cudaMalloc(&p, workspace_bytes());
+        if (e == cudaSuccess) e = cudaMemset(p, 0, workspace_bytes());
         if (e != cudaSuccess) {
             set_error("workspace allocation failed: %s", cudaGetErrorString(e));
             return nullptr;
@@ -54,10 +53,10 @@ int device_sm_count() {
 
 extern "C" int qwen35_b200_status(qwen35_stream_t stream) {
     using namespace q35;
-    Workspace* ws = get_workspace();
+    void* ws = get_workspace();
     if (!ws) return QWEN35_ERR_CUDA;
     int err = 0;
-    Q35_CUDA_OK(cudaMemcpyAsync(&err, &ws->err, sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+    Q35_CUDA_OK(cudaMemcpyAsync(&err, ws, sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream));
     Q35_CUDA_OK(cudaStreamSynchronize((cudaStream_t)stream));
     if (err) set_error("device status %d (%s)", err, err == 1 ? "a bounded device-side wait ran out" : "bad argument seen on device");
     return err;
@@ -65,9 +64,8 @@ extern "C" int qwen35_b200_status(qwen35_stream_t stream) {
 
 extern "C" int qwen35_b200_clear_status(qwen35_stream_t stream) {
     using namespace q35;
-    Workspace* ws = get_workspace();
+    void* ws = get_workspace();
     if (!ws) return QWEN35_ERR_CUDA;
-    // barrier counter, generation and status word restart from zero together
     Q35_CUDA_OK(cudaMemsetAsync(ws, 0, 256, (cudaStream_t)stream));
     return QWEN35_OK;
 }

@@ -9,11 +9,11 @@
 
 namespace q35 {
 
-struct Workspace;
-
 // Workspace of the current device; allocated and zeroed on first use (never inside a capture).
-// Returns nullptr and records an error string on failure.
-Workspace* get_workspace();
+// Its first int is the sticky device status word.  Returns nullptr and records an error string
+// on failure.
+void* get_workspace();
+size_t workspace_bytes();      // defined next to the kernels that lay the workspace out
 
 int device_sm_count();
 void set_error(const char* fmt, ...);
