@@ -85,6 +85,8 @@ typedef struct {
     int n_steps;
     int lm_last_only;          /* 1 = run the LM head only after the last step */
     int dbg_num_layers;        /* 0 = all 24; N>0 stops after N layers (debug) */
+    unsigned long long* dbg_time; /* optional device u64 [25][12]: per-stage %globaltimer stamps of one CTA, last step */
+    int dbg_time_cta;
 } Qwen35DecodeArgs;
 
 int qwen35_b200_decode_steps(const Qwen35DecodeArgs* args, qwen35_stream_t stream);

@@ -35,17 +35,32 @@ struct Smem {
     __align__(16) bf16 x[INTER];                 // GEMV input of the current stage
     __align__(16) bf16 h[HIDDEN];                // raw layer input (residual of stage C)
     __align__(16) bf16 h1[HIDDEN];               // raw mixer output (residual of stage E)
-    float part[256];
+    float part[512];                             // cross-warp partial sums; attention chunk statistics
     float red[NCONS_WARPS];
+    uint32_t stage[64];                          // packed outputs of a stage, published by one coalesced store
     __align__(16) float qk[2][2][DN_K];
     float hd[2][2];
     __align__(16) float q[FA_GQA][FA_HEAD_DIM];
     __align__(16) float kcur[FA_HEAD_DIM];
-    float p[FA_GQA][256];
+    float p[FA_GQA][ATT_CHUNK_MAX];              // scores, then probabilities, of this CTA's chunk
     float ml[FA_GQA][2];
     int abort_flag;
     int tok;
 };
+
+__device__ __forceinline__ unsigned long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+#define Q35_STAMP_ALL(k)                                                                               \
+    do {                                                                                               \
+        if (a.dbg_time) { cons_sync(); Q35_STAMP(k); }                                                  \
+    } while (0)
+#define Q35_STAMP(k)                                                                                   \
+    do {                                                                                               \
+        if (a.dbg_time && last_step && tid == 0) a.dbg_time[((size_t)b * 25 + stamp_row) * 12 + (k)] = gtime(); \
+    } while (0)
 
 __device__ __forceinline__ unsigned epoch_of(const DecodeArgs& a, int step, int slot) {
     return a.epoch_base + 32u * (unsigned)step + (unsigned)slot + 1u;   // slot: 0..23 layer, 24 LM
@@ -57,11 +72,18 @@ __device__ __forceinline__ unsigned epoch_of(const DecodeArgs& a, int step, int 
 __device__ __forceinline__ void produce(const DecodeArgs& a, Smem& s, Ring ring, const Abort& ab) {
     const int b = blockIdx.x, G = gridDim.x;
     const u64 pol = l2_policy_evict_first();
+    long long next_t = clock64();
+    const long long period = a.tma_period;
     auto issue = [&](const void* src, uint32_t bytes) {
         if (ab.on()) return;                       // after an abort nothing new is put in flight
         const unsigned t = ring.t;
         mbar_wait(ring.empty_bar(t), ring.phase(t) ^ 1u, ab);
         if (ab.on()) return;
+        // Pace the stream: a freed ring would otherwise be refilled in one burst by all 148 CTAs at
+        // once, and the latency-critical flagged-word traffic of the next stage queues behind it.
+        long long now = clock64();
+        while (now < next_t) now = clock64();
+        next_t = now + period;
         ring.t = t + 1;
         mbar_arrive_expect_tx(ring.full_bar(t), bytes);
         tma_load_1d(ring.slot_addr(t), src, bytes, ring.full_bar(t), pol);
@@ -154,9 +176,12 @@ __device__ __forceinline__ void consume_k1024(Ring& ring, int n_units, const bf1
 }
 
 __device__ __forceinline__ void poll2(const u64* p0, const u64* p1, uint32_t epoch, const Abort& ab, uint32_t& o0, uint32_t& o1) {
-    const u64 v0 = ld_word(p0), v1 = ld_word(p1);
-    o0 = ((uint32_t)(v0 >> 32) == epoch) ? (uint32_t)v0 : poll_word(p0, epoch, ab);
-    o1 = ((uint32_t)(v1 >> 32) == epoch) ? (uint32_t)v1 : poll_word(p1, epoch, ab);
+    uint32_t o[2];
+    poll_n<2>(p0, (int)(p1 - p0), 2, epoch, ab, o);
+    o0 = o[0]; o1 = o[1];
+}
+__device__ __forceinline__ void poll4(const u64* p, int stride, uint32_t epoch, const Abort& ab, uint32_t (&o)[4]) {
+    poll_n<4>(p, stride, 4, epoch, ab, o);
 }
 
 // RMSNorm(1+w) of 1024 values held one pair per consumer thread; writes bf16 to xs.
@@ -212,6 +237,8 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
 
             for (int layer = 0; layer < n_layers; ++layer) {
                 const LayerRec& L = s.layers[layer];
+                const int stamp_row = layer;
+                Q35_STAMP(0);
                 const unsigned ep = epoch_of(a, step, layer);
                 const bool dn = (L.type == 0);
                 const bf16* w_post = (const bf16*)(dn ? L.p[DN_POST_NORM] : L.p[FA_POST_NORM]);
@@ -239,17 +266,23 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                     reinterpret_cast<uint32_t*>(s.h)[tid] = raw;
                     rmsnorm_pair(raw, (const bf16*)L.p[0], s.x, s.red);
                     cons_sync();
+                    Q35_STAMP(1);
                     const int ntl = dn ? TILES_A_DN : TILES_A_FA;
                     const int u0 = part_begin(ntl, b, G), u1 = part_begin(ntl, b + 1, G);
                     consume_k1024<1>(ring, u1 - u0, s.x, ab, [&](int row, const float (*acc)[2]) {
-                        st_word(&ws->xa[(u0 * 8 + row) >> 1], pack_bf16x2(acc[0][0], acc[0][1]), ep);
+                        s.stage[row >> 1] = pack_bf16x2(acc[0][0], acc[0][1]);
                     });
+                    // one coalesced store per CTA: a line that is written once reaches its pollers fastest
+                    cons_sync();
+                    if (tid < (u1 - u0) * 4) st_word(&ws->xa[u0 * 4 + tid], s.stage[tid], ep);
                 }
 
+                Q35_STAMP_ALL(2);
                 if (dn) {
                     // ================= stage B (DeltaNet): conv, norms, recurrence =================
                     const bf16* conv_w = (const bf16*)L.p[DN_CONV];
                     const int hlo = (2 * pp0) >> 7, hhi = (pp1 > pp0) ? ((2 * pp1 - 1) >> 7) : hlo;   // at most two heads per CTA
+                    uint32_t vw_pre = 0;
                     {
                         // 256 threads: slot (head) x {q,k} x 64 words of two channels
                         const int slot = tid >> 7, isk = (tid >> 6) & 1, wi = tid & 63;
@@ -264,6 +297,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                             c1 = conv_silu(conv_w, ch + 1, s1, bf_hi(xw));
                             sq = rbf(c0 * c0) + rbf(c1 * c1);
                         }
+                        if (my_pair < pp1) vw_pre = poll_word(&ws->xa[(2 * DN_QK_SIZE + 2 * my_pair) >> 1], ep, ab);
                         const float wsum = warp_sum(sq);
                         cons_sync();
                         if (lane == 0) s.red[warp] = wsum;
@@ -300,7 +334,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                         const float4 k4 = *reinterpret_cast<const float4*>(&s.qk[slot][1][lane * 4]);
                         const float beta = s.hd[slot][0], decay = s.hd[slot][1];
                         const int ch = 2 * DN_QK_SIZE + r0;
-                        const uint32_t vw = poll_word(&ws->xa[ch >> 1], ep, ab);
+                        const uint32_t vw = vw_pre;
                         const float vv[2] = {conv_silu(conv_w, ch, cv0, bf_lo(vw)), conv_silu(conv_w, ch + 1, cv1, bf_hi(vw))};
                         float4 sv[2] = {st0, st1};
                         float ov[2];
@@ -317,15 +351,25 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                             ov[r] = warp_sum(o);
                             reinterpret_cast<float4*>(state + (size_t)(r0 + r) * DN_K)[lane] = t;
                         }
-                        if (lane == 0) st_word(&ws->o[my_pair], pack_bf16x2(ov[0], ov[1]), ep);
+                        if (lane == 0) s.stage[warp] = pack_bf16x2(ov[0], ov[1]);
                     }
+                    cons_sync();
+                    if (tid < pp1 - pp0) st_word(&ws->o[pp0 + tid], s.stage[tid], ep);
 
+                    Q35_STAMP(3);
                     // ================= stage C (DeltaNet): gated norm (one head per warp), conv shift =================
                     {
                         const int h = warp;
                         uint32_t o0, o1, z0, z1;
-                        poll2(&ws->o[h * 64 + lane * 2], &ws->o[h * 64 + lane * 2 + 1], ep, ab, o0, o1);
-                        poll2(&ws->xa[(DN_CONV_CH >> 1) + h * 64 + lane * 2], &ws->xa[(DN_CONV_CH >> 1) + h * 64 + lane * 2 + 1], ep, ab, z0, z1);
+                        {
+                            // z was published in stage A, long ago: its loads overlap the wait for `o`
+                            const u64* po = &ws->o[h * 64 + lane * 2];
+                            const u64* pz = &ws->xa[(DN_CONV_CH >> 1) + h * 64 + lane * 2];
+                            const u64 b0 = ld_word(pz), b1 = ld_word(pz + 1);
+                            poll2(po, po + 1, ep, ab, o0, o1);
+                            z0 = ((uint32_t)(b0 >> 32) == ep) ? (uint32_t)b0 : poll_word(pz, ep, ab);
+                            z1 = ((uint32_t)(b1 >> 32) == ep) ? (uint32_t)b1 : poll_word(pz + 1, ep, ab);
+                        }
                         const uint2 nrw = __ldg(reinterpret_cast<const uint2*>(L.p[DN_NORM]) + lane);
                         const float ov[4] = {bf_lo(o0), bf_hi(o0), bf_lo(o1), bf_hi(o1)};
                         const float zv[4] = {bf_lo(z0), bf_hi(z0), bf_lo(z1), bf_hi(z1)};
@@ -341,12 +385,14 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                     }
                     ++i_dn;
                 } else {
-                    // ================= attention: B1 scores, B2 P.V partials, B3 merge + gate =================
+                    // ================= attention: B1 scores + chunk statistics, B2 P.V partials, B3 merge + gate =================
+                    // The context is split into chunks of >= 32 positions; CTA (kv head, chunk) owns one chunk.
                     bf16* kc = a.k_cache + (size_t)i_fa * FA_KV_HEADS * a.max_seq_len * FA_HEAD_DIM;
                     bf16* vc = a.v_cache + (size_t)i_fa * FA_KV_HEADS * a.max_seq_len * FA_HEAD_DIM;
                     const int Lc = pos + 1;
-                    int nchunk = (Lc + 31) / 32; if (nchunk > ATT_MAX_CHUNKS) nchunk = ATT_MAX_CHUNKS;
-                    const int clen = (Lc + nchunk - 1) / nchunk;
+                    int nchunk = (Lc + 31) / 32;
+                    { const int cap = min(ATT_MAX_CHUNKS, G / FA_KV_HEADS); if (nchunk > cap) nchunk = cap; }
+                    const int clen = (Lc + nchunk - 1) / nchunk;            // <= ATT_CHUNK_MAX by the host-side limit on max_seq_len
                     const bool att_cta = b < FA_KV_HEADS * nchunk;
                     const int kvh = b / nchunk, chunk = b % nchunk;
                     const int j0 = chunk * clen, j1 = min(Lc, j0 + clen);
@@ -358,10 +404,11 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                             const int e0 = isq ? (kvh * FA_GQA + warp) * 2 * FA_HEAD_DIM : FA_QPROJ + kvh * FA_HEAD_DIM;
                             const bf16* nw = (const bf16*)(isq ? L.p[FA_QNORM] : L.p[FA_KNORM]);
                             float xv[8], ss = 0.f;
+                            uint32_t wv[4];
+                            poll4(&ws->xa[(e0 >> 1) + lane], 32, ep, ab, wv);
 #pragma unroll
                             for (int i = 0; i < 4; ++i) {
-                                const uint32_t wv = poll_word(&ws->xa[(e0 >> 1) + lane + 32 * i], ep, ab);
-                                xv[2 * i] = bf_lo(wv); xv[2 * i + 1] = bf_hi(wv);
+                                xv[2 * i] = bf_lo(wv[i]); xv[2 * i + 1] = bf_hi(wv[i]);
                                 ss += xv[2 * i] * xv[2 * i] + xv[2 * i + 1] * xv[2 * i + 1];
                             }
                             const float r = rsqrt_ieee(warp_sum(ss) * (1.0f / FA_HEAD_DIM) + RMS_EPS);
@@ -396,67 +443,101 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                             }
                         } else if (warp == FA_GQA + 1 && pos >= j0 && pos < j1) {
                             uint32_t* vrow = reinterpret_cast<uint32_t*>(vc + ((size_t)kvh * a.max_seq_len + pos) * FA_HEAD_DIM);
+                            uint32_t wv[4];
+                            poll4(&ws->xa[((FA_QPROJ + FA_KV_SIZE + kvh * FA_HEAD_DIM) >> 1) + lane], 32, ep, ab, wv);
 #pragma unroll
-                            for (int i = 0; i < 4; ++i)
-                                vrow[lane + 32 * i] = poll_word(&ws->xa[((FA_QPROJ + FA_KV_SIZE + kvh * FA_HEAD_DIM) >> 1) + lane + 32 * i], ep, ab);
+                            for (int i = 0; i < 4; ++i) vrow[lane + 32 * i] = wv[i];
                             __threadfence();
                         }
                         cons_sync();
-                        float qr[FA_GQA][8];
+                        // ---- scores of this chunk, two positions per warp in flight ----
+                        {
+                            float qr[FA_GQA][8];
 #pragma unroll
-                        for (int g = 0; g < FA_GQA; ++g)
+                            for (int g = 0; g < FA_GQA; ++g)
 #pragma unroll
-                            for (int i = 0; i < 8; ++i) qr[g][i] = s.q[g][lane * 8 + i];
-                        for (int j = j0 + warp; j < j1; j += NCONS_WARPS) {
-                            float kf[8];
-                            if (j == pos) {
+                                for (int i = 0; i < 8; ++i) qr[g][i] = s.q[g][lane * 8 + i];
+                            for (int j = j0 + warp; j < j1; j += 2 * NCONS_WARPS) {
+                                const int jb = j + NCONS_WARPS;
+                                uint4 ka = make_uint4(0, 0, 0, 0), kb = ka;
+                                if (j != pos) ka = ld_cg(reinterpret_cast<const uint4*>(kc + ((size_t)kvh * a.max_seq_len + j) * FA_HEAD_DIM) + lane);
+                                if (jb < j1 && jb != pos) kb = ld_cg(reinterpret_cast<const uint4*>(kc + ((size_t)kvh * a.max_seq_len + jb) * FA_HEAD_DIM) + lane);
 #pragma unroll
-                                for (int i = 0; i < 8; ++i) kf[i] = s.kcur[lane * 8 + i];
-                            } else {
-                                unpack8(ld_cg(reinterpret_cast<const uint4*>(kc + ((size_t)kvh * a.max_seq_len + j) * FA_HEAD_DIM) + lane), kf);
-                            }
+                                for (int r = 0; r < 2; ++r) {
+                                    const int jj = r ? jb : j;
+                                    if (jj >= j1) break;
+                                    float kf[8];
+                                    if (jj == pos) {
 #pragma unroll
-                            for (int g = 0; g < FA_GQA; ++g) {
-                                float d = 0.f;
+                                        for (int i = 0; i < 8; ++i) kf[i] = s.kcur[lane * 8 + i];
+                                    } else {
+                                        unpack8(r ? kb : ka, kf);
+                                    }
 #pragma unroll
-                                for (int i = 0; i < 8; ++i) d = fmaf(qr[g][i], kf[i], d);
-                                d = warp_sum(d);
-                                if (lane == 0) st_word(&ws->sc[kvh * FA_GQA + g][j], __float_as_uint(rbf(d) * 0.0625f), ep);
+                                    for (int g = 0; g < FA_GQA; ++g) {
+                                        float d = 0.f;
+#pragma unroll
+                                        for (int i = 0; i < 8; ++i) d = fmaf(qr[g][i], kf[i], d);
+                                        d = warp_sum(d);
+                                        if (lane == 0) s.p[g][jj - j0] = rbf(d) * 0.0625f;
+                                    }
+                                }
                             }
                         }
-                        // ---- B2: softmax statistics over the whole context, then P.V over this chunk ----
+                        cons_sync();
+                        // ---- chunk statistics -> everyone; global max / normaliser from all chunks ----
+                        const int cn = j1 - j0;
                         if (warp < FA_GQA) {
-                            const u64* sc = ws->sc[kvh * FA_GQA + warp];
                             float mx = -INFINITY;
-                            for (int j = lane; j < Lc; j += 32) mx = fmaxf(mx, __uint_as_float(poll_word(sc + j, ep, ab)));
+                            for (int j = lane; j < cn; j += 32) mx = fmaxf(mx, s.p[warp][j]);
                             mx = warp_max(mx);
                             float sm = 0.f;
-                            for (int j = lane; j < Lc; j += 32) sm += expf(__uint_as_float((uint32_t)ld_word(sc + j)) - mx);
+                            for (int j = lane; j < cn; j += 32) sm += expf(s.p[warp][j] - mx);
+                            sm = warp_sum(sm);
+                            if (lane == 0) {
+                                st_word(&ws->att_stat[kvh * FA_GQA + warp][chunk][0], __float_as_uint(mx), ep);
+                                st_word(&ws->att_stat[kvh * FA_GQA + warp][chunk][1], __float_as_uint(sm), ep);
+                            }
+                        }
+                        if (tid < nchunk * FA_GQA * 2) {
+                            const int g = tid / (nchunk * 2), r = tid % (nchunk * 2);
+                            s.part[g * (2 * ATT_MAX_CHUNKS) + r] = __uint_as_float(poll_word(&ws->att_stat[kvh * FA_GQA + g][0][0] + r, ep, ab));
+                        }
+                        cons_sync();
+                        if (warp < FA_GQA) {
+                            const float* st = &s.part[warp * (2 * ATT_MAX_CHUNKS)];
+                            float mx = -INFINITY;
+                            for (int c = lane; c < nchunk; c += 32) mx = fmaxf(mx, st[2 * c]);
+                            mx = warp_max(mx);
+                            float sm = 0.f;
+                            for (int c = lane; c < nchunk; c += 32) sm += st[2 * c + 1] * expf(st[2 * c] - mx);
                             sm = warp_sum(sm);
                             if (lane == 0) { s.ml[warp][0] = mx; s.ml[warp][1] = sm; }
                         }
                         cons_sync();
-                        const int g = tid >> 7, d2 = tid & 127;       // 4 heads x 128 threads, 2 dims each
-                        float acc0 = 0.f, acc1 = 0.f;
-                        for (int t0 = j0; t0 < j1; t0 += 256) {
-                            const int tn = min(256, j1 - t0);
-                            cons_sync();
-                            for (int i = tid; i < FA_GQA * tn; i += NCONS) {
-                                const int gg = i / tn, jj = i % tn;
-                                const float sv = __uint_as_float((uint32_t)ld_word(&ws->sc[kvh * FA_GQA + gg][t0 + jj]));
-                                s.p[gg][jj] = rbf(expf(sv - s.ml[gg][0]) / s.ml[gg][1]);
-                            }
-                            cons_sync();
-                            const uint32_t* vb = reinterpret_cast<const uint32_t*>(vc + ((size_t)kvh * a.max_seq_len + t0) * FA_HEAD_DIM) + d2;
-#pragma unroll 4
-                            for (int jj = 0; jj < tn; ++jj) {
-                                const uint32_t vr = ld_cg(vb + (size_t)jj * (FA_HEAD_DIM / 2));
-                                const float p = s.p[g][jj];
-                                acc0 = fmaf(p, bf_lo(vr), acc0);
-                                acc1 = fmaf(p, bf_hi(vr), acc1);
-                            }
+                        for (int i = tid; i < FA_GQA * cn; i += NCONS) {
+                            const int gg = i / cn, jj = i % cn;
+                            s.p[gg][jj] = rbf(expf(s.p[gg][jj] - s.ml[gg][0]) / s.ml[gg][1]);
                         }
-                        reinterpret_cast<float2*>(ws->att_part[chunk][kvh * FA_GQA + g])[d2] = make_float2(acc0, acc1);
+                        cons_sync();
+                        // ---- P.V over this chunk: 4 heads x 128 threads, 2 dims each, 8 value rows in flight ----
+                        {
+                            const int g = tid >> 7, d2 = tid & 127;
+                            float acc0 = 0.f, acc1 = 0.f;
+                            const uint32_t* vb = reinterpret_cast<const uint32_t*>(vc + ((size_t)kvh * a.max_seq_len + j0) * FA_HEAD_DIM) + d2;
+                            for (int jj = 0; jj < cn; jj += 8) {
+                                uint32_t vr[8];
+#pragma unroll
+                                for (int u = 0; u < 8; ++u) vr[u] = (jj + u < cn) ? ld_cg(vb + (size_t)(jj + u) * (FA_HEAD_DIM / 2)) : 0u;
+#pragma unroll
+                                for (int u = 0; u < 8; ++u) {
+                                    const float p = (jj + u < cn) ? s.p[g][jj + u] : 0.f;
+                                    acc0 = fmaf(p, bf_lo(vr[u]), acc0);
+                                    acc1 = fmaf(p, bf_hi(vr[u]), acc1);
+                                }
+                            }
+                            reinterpret_cast<float2*>(ws->att_part[chunk][kvh * FA_GQA + g])[d2] = make_float2(acc0, acc1);
+                        }
                         __threadfence();
                         cons_sync();
                         if (tid == 0) st_release(&ws->att_flag[kvh][chunk], ep);
@@ -473,20 +554,25 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                         cons_sync();
                         if (tid < 64) {
                             const int d = tid * 4;
-                            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                            for (int c = 0; c < nchunk; ++c) {
-                                const float4 pv = ld_cg(reinterpret_cast<const float4*>(&ws->att_part[c][qh][d]));
-                                acc.x += pv.x; acc.y += pv.y; acc.z += pv.z; acc.w += pv.w;
-                            }
                             uint32_t g0, g1;
                             const int ge = qh * 2 * FA_HEAD_DIM + FA_HEAD_DIM + d;
                             poll2(&ws->xa[ge >> 1], &ws->xa[(ge >> 1) + 1], ep, ab, g0, g1);
+                            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                            for (int c = 0; c < nchunk; c += 8) {
+                                float4 pv[8];
+#pragma unroll
+                                for (int u = 0; u < 8; ++u)
+                                    pv[u] = (c + u < nchunk) ? ld_cg(reinterpret_cast<const float4*>(&ws->att_part[c + u][qh][d])) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                                for (int u = 0; u < 8; ++u) { acc.x += pv[u].x; acc.y += pv[u].y; acc.z += pv[u].z; acc.w += pv[u].w; }
+                            }
                             const float u0 = rbf(acc.x) * rbf(sigmoid_f(bf_lo(g0))), u1 = rbf(acc.y) * rbf(sigmoid_f(bf_hi(g0)));
                             const float u2 = rbf(acc.z) * rbf(sigmoid_f(bf_lo(g1))), u3 = rbf(acc.w) * rbf(sigmoid_f(bf_hi(g1)));
                             st_word(&ws->o[(qh * FA_HEAD_DIM + d) >> 1], pack_bf16x2(u0, u1), ep);
                             st_word(&ws->o[((qh * FA_HEAD_DIM + d) >> 1) + 1], pack_bf16x2(u2, u3), ep);
                         }
                     }
+                    Q35_STAMP(3);
                     // ---- stage C (attention): the gated attention output is the GEMV input ----
                     {
                         uint32_t w0, w1;
@@ -497,19 +583,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                     ++i_fa;
                 }
                 cons_sync();
-                if (dn) {
-                    // this CTA has now seen all of `o`: every CTA finished stage B and nobody reads the
-                    // old conv window of this layer any more -> shift in this token's inputs
-                    for (int c = part_begin(DN_CONV_CH / 2, b, G) + tid; c < part_begin(DN_CONV_CH / 2, b + 1, G); c += NCONS) {
-                        const uint32_t xw = poll_word(&ws->xa[c], ep, ab);
-                        const float4 c0 = ld_cg(reinterpret_cast<const float4*>(conv) + 2 * c);
-                        const float4 c1 = ld_cg(reinterpret_cast<const float4*>(conv) + 2 * c + 1);
-                        reinterpret_cast<float4*>(conv)[2 * c] = make_float4(c0.y, c0.z, c0.w, bf_lo(xw));
-                        reinterpret_cast<float4*>(conv)[2 * c + 1] = make_float4(c1.y, c1.z, c1.w, bf_hi(xw));
-                        __threadfence();
-                    }
-                }
-
+                Q35_STAMP(4);
                 // ---- stage C tail: output projection (K = 2048, 4 rows per tile) + residual ----
                 {
                     const bf16* hin = s.h;
@@ -536,24 +610,50 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                     }
                 }
 
+                Q35_STAMP_ALL(5);
+                if (dn) {
+                    // Conv-window shift, off the critical path.  This CTA has seen all of `o`, so every CTA
+                    // finished stage B and nobody reads this layer's old window any more.  The fence orders the
+                    // new window before this CTA's next publication (stage D), which the next token's readers follow.
+                    for (int c = part_begin(DN_CONV_CH / 2, b, G) + tid; c < part_begin(DN_CONV_CH / 2, b + 1, G); c += NCONS) {
+                        const uint32_t xw = poll_word(&ws->xa[c], ep, ab);
+                        const float4 c0 = ld_cg(reinterpret_cast<const float4*>(conv) + 2 * c);
+                        const float4 c1 = ld_cg(reinterpret_cast<const float4*>(conv) + 2 * c + 1);
+                        reinterpret_cast<float4*>(conv)[2 * c] = make_float4(c0.y, c0.z, c0.w, bf_lo(xw));
+                        reinterpret_cast<float4*>(conv)[2 * c + 1] = make_float4(c1.y, c1.z, c1.w, bf_hi(xw));
+                        __threadfence();
+                    }
+                }
                 // ================= stage D: post norm, gate/up with SiLU*up =================
                 {
                     const uint32_t raw = poll_word(&ws->h1[tid], ep, ab);
                     reinterpret_cast<uint32_t*>(s.h1)[tid] = raw;
                     rmsnorm_pair(raw, w_post, s.x, s.red);
                     cons_sync();
+                    Q35_STAMP(6);
                     const int u0 = part_begin(UNITS_D, b, G), u1 = part_begin(UNITS_D, b + 1, G);
                     consume_k1024<2>(ring, u1 - u0, s.x, ab, [&](int row, const float (*acc)[2]) {
                         const float m0 = rbf(silu_f(rbf(acc[0][0]))) * rbf(acc[1][0]);
                         const float m1 = rbf(silu_f(rbf(acc[0][1]))) * rbf(acc[1][1]);
-                        st_word(&ws->m[(u0 * 8 + row) >> 1], pack_bf16x2(m0, m1), ep);
+                        s.stage[row >> 1] = pack_bf16x2(m0, m1);
                     });
+                    cons_sync();
+                    if (tid < (u1 - u0) * 4) st_word(&ws->m[u0 * 4 + tid], s.stage[tid], ep);
                 }
 
+                Q35_STAMP_ALL(7);
                 // ================= stage E: down projection (K = 3584, 2 rows per tile) + residual =================
                 {
-                    for (int i = tid; i < INTER / 2; i += NCONS) reinterpret_cast<uint32_t*>(s.x)[i] = poll_word(&ws->m[i], ep, ab);
+                    {
+                        // 1792 words: 3 per thread + one more for the first half of the threads
+                        uint32_t mv[4];
+                        const int nw = (tid + 3 * NCONS < INTER / 2) ? 4 : 3;
+                        poll_n<4>(&ws->m[tid], NCONS, nw, ep, ab, mv);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) if (i < nw) reinterpret_cast<uint32_t*>(s.x)[tid + i * NCONS] = mv[i];
+                    }
                     cons_sync();
+                    Q35_STAMP(8);
                     const int u0 = part_begin(TILES_E, b, G), nt = part_begin(TILES_E, b + 1, G) - u0;
                     uint4 xp[7];
 #pragma unroll
@@ -582,12 +682,16 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                         if (last_step && layer == n_layers - 1 && a.hidden_out) reinterpret_cast<uint32_t*>(a.hidden_out)[row >> 1] = hv;
                     }
                 }
+                Q35_STAMP_ALL(9);
             }
 
             // ================= LM head: final norm, 248320 x 1024 GEMV, arg-max =================
             if (!a.lm_last_only || last_step) {
                 const unsigned ep_lm = epoch_of(a, step, 24);
+                const int stamp_row = 24;
+                Q35_STAMP(0);
                 const uint32_t raw = poll_word(&ws->h2[tid], epoch_of(a, step, n_layers - 1), ab);
+                Q35_STAMP(1);
                 rmsnorm_pair(raw, a.final_norm, s.x, s.red);
                 cons_sync();
                 float best = -INFINITY;
@@ -601,6 +705,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                     if (v0 > best) { best = v0; best_i = r0; }
                     if (v1 > best) { best = v1; best_i = r0 + 1; }
                 });
+                Q35_STAMP(2);
                 // lane 0 of every warp holds that warp's best (rows ascend within a warp)
                 cons_sync();
                 if (lane == 0) { s.part[warp] = best; reinterpret_cast<int*>(s.part)[NCONS_WARPS + warp] = best_i; }
@@ -611,24 +716,34 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                         const float v = s.part[w]; const int i = reinterpret_cast<int*>(s.part)[NCONS_WARPS + w];
                         if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
                     }
-                    st_word(&ws->lm[0][b], __float_as_uint(bv), ep_lm);
-                    st_word(&ws->lm[1][b], (uint32_t)bi, ep_lm);
+                    // bf16 value in the high half, row offset inside this CTA's range (< 2048) in the low half
+                    st_word(&ws->lm[0][b], (__float_as_uint(bv) & 0xffff0000u) | (uint32_t)(bi - u0 * 8), ep_lm);
                 }
                 if (warp == 0) {
+                    constexpr int PER = 8;                               // up to 256 CTAs
+                    u64 v[PER];
+#pragma unroll
+                    for (int k = 0; k < PER; ++k) v[k] = (lane + 32 * k < G) ? ld_word(&ws->lm[0][lane + 32 * k]) : 0ull;
                     float bv = -INFINITY; int bi = 0x7fffffff;
-                    for (int c = lane; c < G; c += 32) {
-                        const float v = __uint_as_float(poll_word(&ws->lm[0][c], ep_lm, ab));
-                        const int i = (int)poll_word(&ws->lm[1][c], ep_lm, ab);
-                        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+#pragma unroll
+                    for (int k = 0; k < PER; ++k) {
+                        const int c = lane + 32 * k;
+                        if (c < G) {
+                            const uint32_t w = ((uint32_t)(v[k] >> 32) == ep_lm) ? (uint32_t)v[k] : poll_word(&ws->lm[0][c], ep_lm, ab);
+                            const float val = __uint_as_float(w & 0xffff0000u);
+                            const int idx = part_begin(TILES_LM, c, G) * 8 + (int)(w & 0xffffu);
+                            if (val > bv || (val == bv && idx < bi)) { bv = val; bi = idx; }
+                        }
                     }
 #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) {
-                        const float v = __shfl_xor_sync(0xffffffffu, bv, o); const int i = __shfl_xor_sync(0xffffffffu, bi, o);
-                        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+                        const float v2 = __shfl_xor_sync(0xffffffffu, bv, o); const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+                        if (v2 > bv || (v2 == bv && i2 < bi)) { bv = v2; bi = i2; }
                     }
                     if (lane == 0) s.tok = bi;
                 }
                 cons_sync();
+                Q35_STAMP(3);
                 tok = s.tok;
                 if (b == 0 && tid == 0) {
                     if (a.out_tokens) a.out_tokens[step] = tok;
@@ -671,6 +786,16 @@ static int decode_grid() {
 
 static unsigned g_epoch[64] = {};
 
+static int tma_period() {
+    static int v = -1;
+    if (v < 0) {
+        v = 400;
+        if (const char* s = getenv("QWEN35_TMA_PERIOD")) v = atoi(s);
+        if (v < 0) v = 0;
+    }
+    return v;
+}
+
 static int launch_decode_impl(const DecodeArgs& in, cudaStream_t stream) {
     static std::once_flag once[64];
     static bool ready[64] = {};
@@ -702,7 +827,12 @@ static int launch_decode_impl(const DecodeArgs& in, cudaStream_t stream) {
         set_error("token id %d out of range", a.token_imm);
         return QWEN35_ERR_BAD_ARG;
     }
-    if (device_sm_count() < 64) { set_error("needs at least 64 SMs"); return QWEN35_ERR_UNSUPPORTED; }
+    {
+        const int g = decode_grid();
+        if (g < 64 || g > 256) { set_error("needs between 64 and 256 SMs"); return QWEN35_ERR_UNSUPPORTED; }
+        const int cap = (g / FA_KV_HEADS < ATT_MAX_CHUNKS ? g / FA_KV_HEADS : ATT_MAX_CHUNKS) * ATT_CHUNK_MAX;
+        if (a.max_seq_len > cap) { set_error("max_seq_len %d exceeds %d on this device", a.max_seq_len, cap); return QWEN35_ERR_BAD_ARG; }
+    }
     a.ws = (StreamWorkspace*)get_workspace();
     if (!a.ws) return QWEN35_ERR_CUDA;
     // epochs tag every flagged word; they only ever grow.  On wrap-around the words are cleared.
@@ -712,6 +842,7 @@ static int launch_decode_impl(const DecodeArgs& in, cudaStream_t stream) {
         g_epoch[dev] = 0;
     }
     a.epoch_base = g_epoch[dev];
+    a.tma_period = tma_period();
     g_epoch[dev] += (unsigned)(32u * (unsigned)a.n_steps);
     void* params[] = {(void*)&a};
     Q35_CUDA_OK(cudaLaunchCooperativeKernel((const void*)decode_stream_kernel, dim3(decode_grid()), dim3(STREAM_THREADS), params, sizeof(Smem), stream));
@@ -774,6 +905,8 @@ extern "C" int qwen35_b200_decode_steps(const Qwen35DecodeArgs* in, qwen35_strea
     a.n_steps = in->n_steps;
     a.lm_last_only = in->lm_last_only;
     a.dbg_num_layers = in->dbg_num_layers;
+    a.dbg_time = in->dbg_time;
+    a.dbg_time_cta = in->dbg_time_cta;
     return q35::launch_decode_impl(a, (cudaStream_t)stream);
 }
 

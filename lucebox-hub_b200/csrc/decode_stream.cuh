@@ -14,7 +14,8 @@ namespace q35 {
 typedef unsigned long long u64;
 
 constexpr int MAX_CTX = 32768;          // longest context the decode scratch is sized for
-constexpr int ATT_MAX_CHUNKS = 8;       // split-KV factor of decode attention
+constexpr int ATT_MAX_CHUNKS = 64;      // split-KV factor of decode attention (chunks per kv head)
+constexpr int ATT_CHUNK_MAX = 512;      // longest chunk: MAX_CTX / ATT_MAX_CHUNKS
 
 constexpr int NCONS_WARPS = 16;
 constexpr int NCONS = NCONS_WARPS * 32;             // 512 consumer threads
@@ -42,7 +43,7 @@ struct StreamWorkspace {
     alignas(256) u64 lm[2][1024];                   // per CTA: {bf16 max bits, epoch}, {arg-max, epoch}
     alignas(256) unsigned att_flag[FA_KV_HEADS][ATT_MAX_CHUNKS];
     alignas(256) float att_part[ATT_MAX_CHUNKS][FA_Q_HEADS][FA_HEAD_DIM];
-    alignas(256) u64 sc[FA_Q_HEADS][MAX_CTX];       // attention scores {f32 bits, epoch}
+    alignas(256) u64 att_stat[FA_Q_HEADS][ATT_MAX_CHUNKS][2];   // per head and chunk: {max, epoch}, {sum exp, epoch}
 };
 
 struct DecodeArgs {
@@ -64,12 +65,14 @@ struct DecodeArgs {
     bf16* hidden_out;         // optional [HIDDEN]: last layer's output of the last step
     bf16* dbg_hidden;         // optional [NUM_LAYERS][HIDDEN]: every layer's output of the last step
     const bf16* dbg_teacher;  // optional [NUM_LAYERS][HIDDEN]: input of layer l>0 is row l instead of the previous layer's output
-    bf16* dbg_stage;          // optional: [xa 8224 | o 2048 | h1 1024 | m 3584] of the last layer run
+    unsigned long long* dbg_time;  // optional [25][12]: %globaltimer stamps of CTA dbg_time_cta, last step
+    int dbg_time_cta;
     int position;             // tokens already cached
     int max_seq_len;
     int n_steps;
     int lm_last_only;         // 1: LM head only after the last step (prefill)
     int dbg_num_layers;       // 0 = all; otherwise stop after this many layers
+    int tma_period;           // minimum SM clocks between two weight-tile copies of one CTA (paces the HBM stream)
     unsigned epoch_base;      // epochs used by this launch: epoch_base + 32*step + {1..24 layer, 25 LM}
 };
 
@@ -126,6 +129,9 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 }
 
 constexpr unsigned POLL_LIMIT = 3u * 1000u * 1000u;
+#ifndef POLL_BACKOFF_NS
+#define POLL_BACKOFF_NS 0
+#endif
 
 // Shared abort protocol: the first wait that runs out records an error and raises `*s_abort`;
 // after that no wait blocks, so every thread runs to the end of the kernel and exits normally.
@@ -144,11 +150,35 @@ __device__ __forceinline__ uint32_t poll_word(const u64* p, uint32_t epoch, cons
     if ((uint32_t)(v >> 32) == epoch) return (uint32_t)v;
     unsigned it = 0;
     while (!ab.on()) {
+        if (POLL_BACKOFF_NS) __nanosleep(POLL_BACKOFF_NS);
         v = ld_word(p);
         if ((uint32_t)(v >> 32) == epoch) break;
         if (++it > POLL_LIMIT || ((it & 4095u) == 0 && ld_volatile(ab.g_err) != 0)) { ab.raise(ERR_BARRIER_TIMEOUT); break; }
     }
     return (uint32_t)v;
+}
+
+// N words `stride` apart (only the first `n` are live).  Every round re-issues the loads of all
+// words that are still stale together, so a late producer costs one L2 round trip, not N.
+template <int N>
+__device__ __forceinline__ void poll_n(const u64* p, int stride, int n, uint32_t epoch, const Abort& ab, uint32_t (&o)[N]) {
+    u64 v[N];
+    unsigned pending = 0;
+#pragma unroll
+    for (int i = 0; i < N; ++i) if (i < n) v[i] = ld_word(p + i * stride);
+#pragma unroll
+    for (int i = 0; i < N; ++i) if (i < n && (uint32_t)(v[i] >> 32) != epoch) pending |= 1u << i;
+    unsigned it = 0;
+    while (pending && !ab.on()) {
+        if (POLL_BACKOFF_NS) __nanosleep(POLL_BACKOFF_NS);
+#pragma unroll
+        for (int i = 0; i < N; ++i) if (pending & (1u << i)) v[i] = ld_word(p + i * stride);
+#pragma unroll
+        for (int i = 0; i < N; ++i) if ((pending & (1u << i)) && (uint32_t)(v[i] >> 32) == epoch) pending &= ~(1u << i);
+        if (++it > POLL_LIMIT || ((it & 4095u) == 0 && ld_volatile(ab.g_err) != 0)) { ab.raise(ERR_BARRIER_TIMEOUT); break; }
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i) o[i] = (uint32_t)v[i];
 }
 
 __device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t parity, const Abort& ab) {

@@ -27,7 +27,7 @@ class DecodeArgs(C.Structure):
         ("token_in", C.c_void_p), ("token_imm", C.c_int),
         ("forced_ids", C.c_void_p), ("out_token", C.c_void_p), ("out_tokens", C.c_void_p),
         ("logits_out", C.c_void_p), ("hidden_out", C.c_void_p), ("dbg_hidden", C.c_void_p), ("dbg_teacher", C.c_void_p),
-        ("position", C.c_int), ("max_seq_len", C.c_int), ("n_steps", C.c_int), ("lm_last_only", C.c_int), ("dbg_num_layers", C.c_int),
+        ("position", C.c_int), ("max_seq_len", C.c_int), ("n_steps", C.c_int), ("lm_last_only", C.c_int), ("dbg_num_layers", C.c_int), ("dbg_time", C.c_void_p), ("dbg_time_cta", C.c_int),
     ]
 
 

@@ -151,7 +151,7 @@ class Decoder:
         self._position += 1
         return int(self._out_token.item())
 
-    def step_many(self, token_id: int, num_steps: int, logits_out=None) -> torch.Tensor:
+    def step_many(self, token_id: int, num_steps: int, logits_out=None, dbg_time=None, dbg_time_cta=0) -> torch.Tensor:
         """`num_steps` greedy steps in one launch, tokens fed back on the device
         (model.py:716-743 offers this for NVFP4 only).  Returns int32 [num_steps] on the GPU."""
         if num_steps < 0:
@@ -160,7 +160,7 @@ class Decoder:
         if num_steps == 0:
             return out
         a = self._args(token_imm=int(token_id), n_steps=num_steps, out_tokens=out.data_ptr(),
-                       logits_out=_capi.ptr(logits_out))
+                       logits_out=_capi.ptr(logits_out), dbg_time=_capi.ptr(dbg_time), dbg_time_cta=dbg_time_cta)
         self._run(a)
         self._position += num_steps
         return out
