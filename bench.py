@@ -286,7 +286,7 @@ def run_ours(args):
         traffic = None
         try:
             with open(os.path.join(ROOT, "profiles", "decode_bf16_traffic.json")) as f:
-                traffic = json.load(f).get("dram_bytes_per_launch_tg128")
+                traffic = json.load(f)["dram_bytes_per_token"] * GEN
         except Exception:
             pass
         line = {
@@ -299,7 +299,7 @@ def run_ours(args):
             "pp520_vs_baseline": PROMPT / (min(pp_ms) * 1e-3) / BASELINE_PP520,
             "pp520_note": "token-serial prefill through the decode megakernel",
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_kind": peak_kind, "traffic": traffic, "kernel": "decode_bf16_kernel",
+                         "peak_kind": peak_kind, "traffic": traffic, "kernel": "decode_stream_kernel",
                          "algorithmic_bytes_per_launch": alg_bytes, "launch_ms": kern_avg},
             "e2e": {"value": world * GEN * e2e_steps / (e2e_ms * 1e-3), "unit": "tok/s",
                     "h2d_bytes_per_step": GEN * 4, "d2h_bytes_per_step": GEN * 4,

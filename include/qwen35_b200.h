@@ -91,6 +91,13 @@ typedef struct {
 
 int qwen35_b200_decode_steps(const Qwen35DecodeArgs* args, qwen35_stream_t stream);
 
+/* BF16 GEMM on tcgen05/TMEM tensor cores: C[M,N] = epi(A[M,K] . B[b_rows,K]^T), f32 accumulate, one
+ * rounding to bf16.  Replaces cublas_bf16_gemm (prefill.cu:895-903).  lda/ldc/ldr are row strides in
+ * elements; K must be a multiple of 64.  epilogue: 0 = store, 1 = + R (residual, bf16 add),
+ * 2 = silu(gate)*up where gate = B rows [0,N) and up = B rows [up_row_offset, up_row_offset+N). */
+int qwen35_b200_gemm_bf16(const void* A, int lda, const void* B, int b_rows, void* C, int ldc, const void* R, int ldr,
+                          int M, int N, int K, int epilogue, int up_row_offset, qwen35_stream_t stream);
+
 /* Synchronises `stream`, then returns the sticky device status word of the current device
  * (QWEN35_OK, or the first error a kernel recorded).  qwen35_b200_clear_status() re-arms the
  * library after an error. */

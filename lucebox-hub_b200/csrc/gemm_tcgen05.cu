@@ -1,0 +1,308 @@
+// BF16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM) fed by TMA, for the prefill
+// projections:  C[M,N] = A[M,K] . B[N,K]^T  with f32 accumulation in tensor memory.
+//
+// Replaces the cuBLAS calls of the reference's prefill (cublas_bf16_gemm, prefill.cu:895-903 and its
+// ten call sites :1267-1434).  One CTA computes one 128 x 128 output tile:
+//   warp 0     TMA producer: 128B-swizzled 64-wide K slices of A and B into a 6-stage ring
+//   warp 1     allocates 128 TMEM columns, then one thread issues tcgen05.mma (M128 N128 K16 x4 per
+//              stage) and commits each stage back to the producer
+//   warps 2-5  epilogue: tcgen05.ld the accumulator rows, round once to bf16 (what a bf16 linear
+//              layer returns), optionally fuse the residual add or silu(gate)*up, store
+// Every wait is bounded; a wait that runs out sets the status word and the CTA unwinds normally.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "runtime.h"
+
+namespace q35 {
+
+constexpr int GEMM_BM = 128, GEMM_BN = 128, GEMM_BK = 64, GEMM_STAGES = 6;
+constexpr int GEMM_THREADS = 192;
+constexpr uint32_t GEMM_STAGE_BYTES = (GEMM_BM + GEMM_BN) * GEMM_BK * 2;   // 32 KB
+constexpr uint32_t GEMM_SMEM = GEMM_STAGES * GEMM_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr unsigned GEMM_SPIN_LIMIT = 20u * 1000u * 1000u;
+
+enum GemmEpi { EPI_BF16 = 0, EPI_RESIDUAL = 1, EPI_SILU_MUL = 2 };
+
+struct GemmParams {
+    int M, N, K;            // N counts output columns
+    bf16* C; int ldc;
+    const bf16* R; int ldr; // residual (EPI_RESIDUAL)
+    int up_row_offset;      // EPI_SILU_MUL: B row of "up" = up_row_offset + column
+    int* err;
+};
+
+__device__ __forceinline__ uint32_t g_smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void g_mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void g_mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool g_mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+// bounded wait; returns false (and records the error) when the limit is hit
+__device__ __forceinline__ bool g_mbar_wait(uint32_t bar, uint32_t parity, int* err, volatile int* s_abort) {
+    unsigned it = 0;
+    while (!g_mbar_try_wait(bar, parity)) {
+        if (*s_abort) return false;
+        if (++it > GEMM_SPIN_LIMIT) { *s_abort = 1; atomicCAS(err, 0, (int)ERR_BARRIER_TIMEOUT); return false; }
+    }
+    return true;
+}
+__device__ __forceinline__ void g_tma_load_2d(uint32_t dst, const CUtensorMap* tm, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(tm), "r"(x), "r"(y), "r"(bar) : "memory");
+}
+
+// 64-bit shared-memory matrix descriptor, K-major operand, 128-byte swizzle:
+// start address >> 4 | LBO (unused for this layout) | SBO = 1024 B between 8-row groups | version 1 | layout 2
+__device__ __forceinline__ uint64_t make_smem_desc(uint32_t smem_addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)(1024 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+// instruction descriptor: D f32, A/B bf16, both K-major, N at [17,23) in units of 8, M at [24,29) in units of 16
+constexpr uint32_t GEMM_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(GEMM_BN >> 3) << 17) | ((uint32_t)(GEMM_BM >> 4) << 24);
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr) : "memory");
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+    extern __shared__ unsigned char g_smem_raw[];
+    // 128B-swizzled tiles need 1024-byte alignment
+    const uint32_t raw = g_smem_u32(g_smem_raw);
+    const uint32_t tiles = (raw + 1023u) & ~1023u;
+    unsigned char* tiles_ptr = g_smem_raw + (tiles - raw);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(tiles_ptr + GEMM_STAGES * GEMM_STAGE_BYTES);
+    const uint32_t full0 = g_smem_u32(bars), empty0 = full0 + 8 * GEMM_STAGES, tfull = empty0 + 8 * GEMM_STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * GEMM_STAGES + 1);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int BN_OUT = (EPI == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
+    const int n0 = blockIdx.x * BN_OUT, m0 = blockIdx.y * GEMM_BM;
+    const int nkb = p.K / GEMM_BK;
+
+    if (threadIdx.x == 0) {
+        *s_abort = 0;
+        for (int i = 0; i < GEMM_STAGES; ++i) { g_mbar_init(full0 + 8 * i, 1); g_mbar_init(empty0 + 8 * i, 1); }
+        g_mbar_init(tfull, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(g_smem_u32(tmem_slot)), "r"(128u) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int issued = 0;
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int st = kb % GEMM_STAGES;
+                if (!g_mbar_wait(empty0 + 8 * st, ((kb / GEMM_STAGES) & 1) ^ 1, p.err, s_abort)) break;
+                const uint32_t a_dst = tiles + st * GEMM_STAGE_BYTES, b_dst = a_dst + GEMM_BM * GEMM_BK * 2;
+                g_mbar_expect_tx(full0 + 8 * st, GEMM_STAGE_BYTES);
+                g_tma_load_2d(a_dst, &tmA, kb * GEMM_BK, m0, full0 + 8 * st);
+                if (EPI == EPI_SILU_MUL) {
+                    g_tma_load_2d(b_dst, &tmB, kb * GEMM_BK, n0, full0 + 8 * st);
+                    g_tma_load_2d(b_dst + 64 * GEMM_BK * 2, &tmB, kb * GEMM_BK, p.up_row_offset + n0, full0 + 8 * st);
+                } else {
+                    g_tma_load_2d(b_dst, &tmB, kb * GEMM_BK, n0, full0 + 8 * st);
+                    g_tma_load_2d(b_dst + 64 * GEMM_BK * 2, &tmB, kb * GEMM_BK, n0 + 64, full0 + 8 * st);
+                }
+                issued = kb + 1;
+            }
+            // every copy this CTA issued must have landed before it may exit (matters only after an abort)
+            if (*s_abort) {
+                for (int kb = max(0, issued - GEMM_STAGES); kb < issued; ++kb) {
+                    unsigned it = 0;
+                    while (!g_mbar_try_wait(full0 + 8 * (kb % GEMM_STAGES), (kb / GEMM_STAGES) & 1) && ++it < GEMM_SPIN_LIMIT) {}
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            bool ok = true;
+            for (int kb = 0; kb < nkb && ok; ++kb) {
+                const int st = kb % GEMM_STAGES;
+                ok = g_mbar_wait(full0 + 8 * st, (kb / GEMM_STAGES) & 1, p.err, s_abort);
+                if (!ok) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t a_addr = tiles + st * GEMM_STAGE_BYTES, b_addr = a_addr + GEMM_BM * GEMM_BK * 2;
+                const uint64_t adesc = make_smem_desc(a_addr), bdesc = make_smem_desc(b_addr);
+#pragma unroll
+                for (int k = 0; k < GEMM_BK / 16; ++k)   // 32 bytes of K per instruction: advance the start-address field by 2
+                    umma_bf16(tmem_base, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), GEMM_IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+                umma_commit(empty0 + 8 * st);       // frees the stage when these MMAs have read it
+            }
+            umma_commit(tfull);                     // accumulator complete (also fires after an abort so the epilogue wakes)
+        }
+    } else {
+        // ---- epilogue: warp w may touch TMEM lanes [32*(w%4), +32) ----
+        const int q = warp & 3;
+        const int row = m0 + q * 32 + lane;
+        const bool ok = g_mbar_wait(tfull, 0, p.err, s_abort) && !*s_abort;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (ok) {
+            if (EPI == EPI_SILU_MUL) {
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t g[32], u[32];
+                    tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), g);
+                    tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(64 + c * 32), u);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                    if (row < p.M) {
+                        bf16* dst = p.C + (size_t)row * p.ldc + n0 + c * 32;
+#pragma unroll
+                        for (int j = 0; j < 32; j += 2) {
+                            const int n = n0 + c * 32 + j;
+                            const float m0v = rbf(silu_f(rbf(__uint_as_float(g[j])))) * rbf(__uint_as_float(u[j]));
+                            const float m1v = rbf(silu_f(rbf(__uint_as_float(g[j + 1])))) * rbf(__uint_as_float(u[j + 1]));
+                            if (n + 1 < p.N) *reinterpret_cast<__nv_bfloat162*>(dst + j) = __halves2bfloat162(f2bf(m0v), f2bf(m1v));
+                            else if (n < p.N) dst[j] = f2bf(m0v);
+                        }
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < GEMM_BN / 32; ++c) {
+                    uint32_t v[32];
+                    tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                    if (row < p.M) {
+                        bf16* dst = p.C + (size_t)row * p.ldc + n0 + c * 32;
+                        const bf16* res = (EPI == EPI_RESIDUAL) ? p.R + (size_t)row * p.ldr + n0 + c * 32 : nullptr;
+#pragma unroll
+                        for (int j = 0; j < 32; j += 2) {
+                            const int n = n0 + c * 32 + j;
+                            float y0 = rbf(__uint_as_float(v[j])), y1 = rbf(__uint_as_float(v[j + 1]));
+                            if (EPI == EPI_RESIDUAL) {
+                                if (n < p.N) y0 += bf2f(res[j]);
+                                if (n + 1 < p.N) y1 += bf2f(res[j + 1]);
+                            }
+                            if (n + 1 < p.N) *reinterpret_cast<__nv_bfloat162*>(dst + j) = __halves2bfloat162(f2bf(y0), f2bf(y1));
+                            else if (n < p.N) dst[j] = f2bf(y0);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(128u) : "memory");
+    }
+}
+
+// ---------------------------------------- host side -------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                                  const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult qres;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &qres) == cudaSuccess && qres == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    }
+    return fn;
+}
+
+// 2-D bf16 tensor [rows, cols] with row stride `ld` elements; box = 64 columns x box_rows, 128-byte swizzle.
+static bool make_tmap(CUtensorMap* tm, const void* ptr, int rows, int cols, int ld, int box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// C[M,N] (row stride ldc) = epi(A[M,K] (row stride lda) . B[*,K]^T).  epi: 0 bf16, 1 + R, 2 silu(gate)*up with
+// gate rows [0,N) and up rows [up_row_offset, up_row_offset+N) of B.  b_rows = number of rows of B.
+int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ldc, const bf16* R, int ldr,
+              int M, int N, int K, int epi, int up_row_offset, cudaStream_t stream) {
+    if (M <= 0 || N <= 0) return QWEN35_OK;
+    if (K % GEMM_BK != 0 || (lda % 8) != 0 || ((uintptr_t)A & 15) || ((uintptr_t)B & 15)) {
+        set_error("gemm_bf16: K must be a multiple of 64 and operands 16-byte aligned");
+        return QWEN35_ERR_BAD_ARG;
+    }
+    void* ws = get_workspace();
+    if (!ws) return QWEN35_ERR_CUDA;
+    CUtensorMap tmA, tmB;
+    if (!make_tmap(&tmA, A, M, K, lda, GEMM_BM) || !make_tmap(&tmB, B, b_rows, K, K, 64)) {
+        set_error("cuTensorMapEncodeTiled failed");
+        return QWEN35_ERR_CUDA;
+    }
+    GemmParams p{M, N, K, C, ldc, R, ldr, up_row_offset, (int*)ws};
+    static bool attr_done = false;
+    if (!attr_done) {
+        Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<EPI_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM));
+        Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<EPI_RESIDUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM));
+        Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<EPI_SILU_MUL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM));
+        attr_done = true;
+    }
+    const int bn_out = (epi == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
+    dim3 grid((N + bn_out - 1) / bn_out, (M + GEMM_BM - 1) / GEMM_BM);
+    switch (epi) {
+        case EPI_BF16: gemm_bf16_tcgen05_kernel<EPI_BF16><<<grid, GEMM_THREADS, GEMM_SMEM, stream>>>(tmA, tmB, p); break;
+        case EPI_RESIDUAL: gemm_bf16_tcgen05_kernel<EPI_RESIDUAL><<<grid, GEMM_THREADS, GEMM_SMEM, stream>>>(tmA, tmB, p); break;
+        case EPI_SILU_MUL: gemm_bf16_tcgen05_kernel<EPI_SILU_MUL><<<grid, GEMM_THREADS, GEMM_SMEM, stream>>>(tmA, tmB, p); break;
+        default: set_error("gemm_bf16: unknown epilogue %d", epi); return QWEN35_ERR_BAD_ARG;
+    }
+    Q35_CUDA_OK(cudaGetLastError());
+    g_launches.fetch_add(1);
+    return QWEN35_OK;
+}
+
+}  // namespace q35
+
+extern "C" int qwen35_b200_gemm_bf16(const void* A, int lda, const void* B, int b_rows, void* C, int ldc, const void* R, int ldr,
+                                     int M, int N, int K, int epilogue, int up_row_offset, qwen35_stream_t stream) {
+    return q35::gemm_bf16((const q35::bf16*)A, lda, (const q35::bf16*)B, b_rows, (q35::bf16*)C, ldc, (const q35::bf16*)R, ldr,
+                          M, N, K, epilogue, up_row_offset, (cudaStream_t)stream);
+}

@@ -38,6 +38,7 @@ _vp, _i = C.c_void_p, C.c_int
 SIGNATURES = {
     "launch_decode": (_i, [_i, _vp] + [_vp] * 8 + [_vp] * 11 + [_vp] * 5 + [_i, _i, _vp]),
     "qwen35_b200_decode_steps": (_i, [C.POINTER(DecodeArgs), _vp]),
+    "qwen35_b200_gemm_bf16": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "qwen35_b200_status": (_i, [_vp]),
     "qwen35_b200_clear_status": (_i, [_vp]),
     "qwen35_b200_debug_read": (_i, [_i, _vp]),
