@@ -91,6 +91,49 @@ typedef struct {
 
 int qwen35_b200_decode_steps(const Qwen35DecodeArgs* args, qwen35_stream_t stream);
 
+/* Replaces launch_prefill_bf16 (torch_bindings.cpp:323-335; prefill.cu:1158-1497): batched prefill of
+ * `seq_len` prompt tokens from a zeroed state.  Fills the KV cache rows [0, seq_len), the DeltaNet states and
+ * conv windows, writes the last token's hidden state to hidden_bf16_out and arg-max(logits) to output_token.
+ * Scratch buffers have the sizes the reference's Decoder allocates (model.py:569-602); proj_buf_half,
+ * proj_act_packed and proj_act_scales belong to the reference's NVFP4 option and are ignored.  `fused_layers`
+ * is the device table of PrefillFusedLayerWeights records (6 pointers per layer, prefill.cu:66-73).  The cache
+ * length is the reference's fixed 2048; use qwen35_b200_prefill_bf16 for other lengths. */
+int launch_prefill_bf16(
+    const int* token_ids, int seq_len, int* output_token,
+    const void* embed_weight, const LayerWeights* layers, const void* fused_layers,
+    const void* final_norm_w, const void* lm_head_w,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* hidden, void* residual, void* normalized,
+    void* proj_buf, void* proj_buf2, void* proj_buf_half, void* proj_act_packed, void* proj_act_scales,
+    void* attn_buf, void* mlp_buf, void* dn_out_buf, void* beta_buf, void* alpha_buf,
+    void* final_normed, void* hidden_bf16_out, void* lm_bmv, void* lm_bmi, qwen35_stream_t stream);
+
+/* The same with an explicit cache length, optional logits and a layer limit for tests. */
+typedef struct {
+    const int* token_ids; int seq_len; int* out_token;
+    const void* embed_weight; const LayerWeights* layer_weights; const void* fused_layer_weights;
+    const void* final_norm_weight; const void* lm_head_weight;
+    void* fa_k_cache; void* fa_v_cache; void* dn_states; void* conv_bufs;
+    void* hidden;        /* bf16 [S,1024]: layer input / output */
+    void* residual;      /* bf16 [S,1024]: hidden after the mixer residual */
+    void* normalized;    /* bf16 [S,1024] */
+    void* proj_buf;      /* bf16 [S,8320] */
+    void* proj_buf2;     /* bf16 [S,6144] */
+    void* attn_buf;      /* bf16 [S,2048] */
+    void* mlp_buf;       /* bf16 [S,3584] */
+    void* dn_out_buf;    /* bf16 [S,2048] */
+    void* beta_buf;      /* f32 [S,16] */
+    void* alpha_buf;     /* f32 [S,16] */
+    void* final_normed;  /* bf16 [1024] */
+    void* hidden_bf16_out; /* bf16 [1024] */
+    void* lm_bmv;        /* f32 [1024] */
+    void* lm_bmi;        /* i32 [1024] */
+    float* logits_out;   /* optional f32 [248320] */
+    int max_seq_len;
+    int dbg_num_layers;  /* 0 = all */
+} Qwen35PrefillArgs;
+int qwen35_b200_prefill_bf16(const Qwen35PrefillArgs* args, qwen35_stream_t stream);
+
 /* BF16 GEMM on tcgen05/TMEM tensor cores: C[M,N] = epi(A[M,K] . B[b_rows,K]^T), f32 accumulate, one
  * rounding to bf16.  Replaces cublas_bf16_gemm (prefill.cu:895-903).  lda/ldc/ldr are row strides in
  * elements; K must be a multiple of 64.  epilogue: 0 = store, 1 = + R (residual, bf16 add),

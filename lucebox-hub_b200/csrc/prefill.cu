@@ -1,0 +1,207 @@
+// Host orchestration of the BF16 prefill: per layer RMSNorm -> fused projection GEMM (tcgen05) ->
+// DeltaNet (prep, chunk-local solve, scan over chunks, gated norm) or attention (q/k norm + RoPE +
+// KV fill, causal attention) -> output GEMM + residual -> RMSNorm -> gate/up GEMM with fused
+// SiLU*up -> down GEMM + residual; then the last token's final norm and LM-head arg-max.
+//
+// Replaces launch_prefill_bf16 / launch_prefill_bf16_impl of the reference (prefill.cu:1158-1497,
+// declared torch_bindings.cpp:323-335).  Nothing here synchronises or copies to the host, so the
+// call can be captured in a CUDA graph once the library scratch has reached its size (first call).
+#include "prefill_kernels.cuh"
+
+#include <cmath>
+#include <mutex>
+
+#include "runtime.h"
+
+namespace q35 {
+
+int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ldc, const bf16* R, int ldr,
+              int M, int N, int K, int epi, int up_row_offset, cudaStream_t stream);
+
+struct PrefillFused {            // reference: struct PrefillFusedLayerWeights (torch_bindings.cpp:31-38, prefill.cu:66-73)
+    const void* proj_weight;     // DN: [qkv; z; b; a] = 8224 x 1024, FA: [q; k; v] = 5120 x 1024
+    const void* gate_up_weight;  // [gate; up] = 7168 x 1024
+    const void* unused[4];       // NVFP4 copies of the same matrices (not read by the BF16 path)
+};
+
+// grow-only per-device scratch for the chunk-local results
+static void* g_scratch[64] = {};
+static size_t g_scratch_bytes[64] = {};
+static std::mutex g_scratch_mu;
+
+static void* get_scratch(size_t bytes) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    dev &= 63;
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (g_scratch_bytes[dev] < bytes) {
+        if (g_scratch[dev]) { cudaDeviceSynchronize(); cudaFree(g_scratch[dev]); g_scratch[dev] = nullptr; g_scratch_bytes[dev] = 0; }
+        if (cudaMalloc(&g_scratch[dev], bytes) != cudaSuccess) { set_error("prefill scratch allocation of %zu bytes failed", bytes); return nullptr; }
+        g_scratch_bytes[dev] = bytes;
+    }
+    return g_scratch[dev];
+}
+
+struct PrefillArgs {
+    const int* token_ids; int S; int* out_token;
+    const bf16* embed; const LayerRec* layers_host; const PrefillFused* fused_host;
+    const bf16* final_norm; const bf16* lm_head;
+    bf16* k_cache; bf16* v_cache; float* dn_states; float* conv_bufs;
+    bf16 *hidden, *residual, *normalized, *proj_buf, *proj_buf2, *attn_buf, *mlp_buf, *dn_out_buf;
+    float *beta_buf, *alpha_buf;
+    bf16 *final_normed, *hidden_out;
+    float* lm_bmv; int* lm_bmi;
+    float* logits_out;
+    int max_seq_len;
+    int n_layers;
+};
+
+#define Q35_TRY(expr)                        \
+    do {                                     \
+        const int st__ = (expr);             \
+        if (st__ != QWEN35_OK) return st__;  \
+    } while (0)
+
+static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
+    const int S = a.S;
+    static bool attr_done = false;
+    if (!attr_done) {
+        Q35_CUDA_OK(cudaFuncSetAttribute(pf_dn_chunk_local_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CHUNK_LOCAL_SMEM));
+        Q35_CUDA_OK(cudaFuncSetAttribute(pf_dn_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CHUNK_SCAN_SMEM));
+        Q35_CUDA_OK(cudaFuncSetAttribute(pf_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)((ATT_PF_WARPS * ATT_PF_MAX_S + ATT_PF_WARPS * FA_HEAD_DIM) * sizeof(float))));
+        attr_done = true;
+    }
+    const int nchunks = (S + DN_CHUNK - 1) / DN_CHUNK;
+    ChunkScratch* scratch = (ChunkScratch*)get_scratch((size_t)DN_HEADS * nchunks * sizeof(ChunkScratch));
+    if (!scratch) return QWEN35_ERR_CUDA;
+    RopeTable rt;
+    for (int i = 0; i < FA_ROT / 2; ++i) rt.f[i] = 1.0f / (float)std::pow(1.0e7, (double)((float)(2 * i) / (float)FA_ROT));
+
+    int i_dn = 0, i_fa = 0;
+    for (int layer = 0; layer < a.n_layers; ++layer) {
+        const LayerRec& L = a.layers_host[layer];
+        const PrefillFused& F = a.fused_host[layer];
+        // input norm (layer 0 gathers the embedding rows into `hidden` on the way)
+        pf_rmsnorm_kernel<<<S, 128, 0, stream>>>(layer == 0 ? a.token_ids : nullptr, a.embed, a.hidden, (const bf16*)L.p[0],
+                                                 layer == 0 ? a.hidden : nullptr, a.normalized, S);
+        g_launches.fetch_add(1);
+        const bf16 *w_out, *w_post, *w_down;
+        if (L.type == 0) {
+            const int ldp = DN_PROJ_ROWS;
+            Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)F.proj_weight, DN_PROJ_ROWS, a.proj_buf, ldp, nullptr, 0, S, DN_PROJ_ROWS, HIDDEN, 0, 0, stream));
+            pf_dn_prep_kernel<<<dim3(S, DN_HEADS), 128, 0, stream>>>(a.proj_buf, ldp, (const bf16*)L.p[DN_CONV], (const bf16*)L.p[DN_ALOG],
+                                                                      (const bf16*)L.p[DN_DTBIAS], a.proj_buf2, a.beta_buf, a.alpha_buf, S);
+            pf_conv_state_kernel<<<(DN_CONV_CH + 255) / 256, 256, 0, stream>>>(a.proj_buf, ldp, a.conv_bufs + (size_t)i_dn * DN_CONV_CH * 4, S);
+            pf_dn_chunk_local_kernel<<<dim3(nchunks, DN_HEADS), 256, CHUNK_LOCAL_SMEM, stream>>>(a.proj_buf2, a.beta_buf, a.alpha_buf, scratch, S, nchunks);
+            pf_dn_chunk_scan_kernel<<<dim3(DN_HEADS, DN_V / SCAN_VW), 256, CHUNK_SCAN_SMEM, stream>>>(
+                a.proj_buf2, scratch, a.dn_out_buf, a.dn_states + (size_t)i_dn * DN_HEADS * DN_V * DN_K, S, nchunks);
+            pf_gated_norm_kernel<<<(S * DN_HEADS + 7) / 8, 256, 0, stream>>>(a.dn_out_buf, a.proj_buf, ldp, (const bf16*)L.p[DN_NORM], a.attn_buf, S);
+            g_launches.fetch_add(5);
+            w_out = (const bf16*)L.p[DN_OUT]; w_post = (const bf16*)L.p[DN_POST_NORM]; w_down = (const bf16*)L.p[DN_DOWN];
+            ++i_dn;
+        } else {
+            const int ldp = FA_PROJ_ROWS;
+            Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)F.proj_weight, FA_PROJ_ROWS, a.proj_buf, ldp, nullptr, 0, S, FA_PROJ_ROWS, HIDDEN, 0, 0, stream));
+            bf16* kc = a.k_cache + (size_t)i_fa * FA_KV_HEADS * a.max_seq_len * FA_HEAD_DIM;
+            bf16* vc = a.v_cache + (size_t)i_fa * FA_KV_HEADS * a.max_seq_len * FA_HEAD_DIM;
+            pf_qk_norm_rope_kernel<<<(S * 12 + 7) / 8, 256, 0, stream>>>(a.proj_buf, ldp, (const bf16*)L.p[FA_QNORM], (const bf16*)L.p[FA_KNORM], rt,
+                                                                         a.proj_buf2, kc, vc, S, a.max_seq_len);
+            const size_t att_smem = ((size_t)ATT_PF_WARPS * S + ATT_PF_WARPS * FA_HEAD_DIM) * sizeof(float);
+            pf_attention_kernel<<<dim3((S + ATT_PF_WARPS - 1) / ATT_PF_WARPS, FA_Q_HEADS), ATT_PF_WARPS * 32, att_smem, stream>>>(
+                a.proj_buf2, kc, vc, a.proj_buf, ldp, a.attn_buf, S, a.max_seq_len);
+            g_launches.fetch_add(2);
+            w_out = (const bf16*)L.p[FA_O]; w_post = (const bf16*)L.p[FA_POST_NORM]; w_down = (const bf16*)L.p[FA_DOWN];
+            ++i_fa;
+        }
+        // output projection + residual -> residual buffer holds the hidden state after the mixer
+        Q35_TRY(gemm_bf16(a.attn_buf, 2048, w_out, HIDDEN, a.residual, HIDDEN, a.hidden, HIDDEN, S, HIDDEN, 2048, 1, 0, stream));
+        pf_rmsnorm_kernel<<<S, 128, 0, stream>>>(nullptr, nullptr, a.residual, w_post, nullptr, a.normalized, S);
+        g_launches.fetch_add(1);
+        Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)F.gate_up_weight, 2 * INTER, a.mlp_buf, INTER, nullptr, 0, S, INTER, HIDDEN, 2, INTER, stream));
+        Q35_TRY(gemm_bf16(a.mlp_buf, INTER, w_down, HIDDEN, a.hidden, HIDDEN, a.residual, HIDDEN, S, HIDDEN, INTER, 1, 0, stream));
+    }
+    // last token: final norm, LM head, arg-max
+    const bf16* last = a.hidden + (size_t)(S - 1) * HIDDEN;
+    if (a.hidden_out) Q35_CUDA_OK(cudaMemcpyAsync(a.hidden_out, last, HIDDEN * sizeof(bf16), cudaMemcpyDeviceToDevice, stream));
+    pf_rmsnorm_kernel<<<1, 128, 0, stream>>>(nullptr, nullptr, last, a.final_norm, nullptr, a.final_normed, 1);
+    const int lm_blocks = 592;
+    pf_lm_head_kernel<<<lm_blocks, 256, 0, stream>>>(a.final_normed, a.lm_head, a.lm_bmv, a.lm_bmi, a.logits_out);
+    pf_lm_reduce_kernel<<<1, 32, 0, stream>>>(a.lm_bmv, a.lm_bmi, lm_blocks, a.out_token);
+    g_launches.fetch_add(3);
+    Q35_CUDA_OK(cudaGetLastError());
+    return QWEN35_OK;
+}
+
+// The layer tables live in device memory (the reference's packed blobs).  They are read back once
+// per distinct table pointer and kept on the host, as the reference does (prefill.cu:1179-1195).
+struct HostTables { const void* dev_layers; const void* dev_fused; LayerRec layers[NUM_LAYERS]; PrefillFused fused[NUM_LAYERS]; };
+static HostTables g_tables[8];
+static int g_tables_n = 0;
+static std::mutex g_tables_mu;
+
+static const HostTables* host_tables(const void* dev_layers, const void* dev_fused) {
+    std::lock_guard<std::mutex> lk(g_tables_mu);
+    for (int i = 0; i < g_tables_n; ++i)
+        if (g_tables[i].dev_layers == dev_layers && g_tables[i].dev_fused == dev_fused) return &g_tables[i];
+    HostTables* t = &g_tables[g_tables_n < 8 ? g_tables_n++ : 7];
+    t->dev_layers = dev_layers; t->dev_fused = dev_fused;
+    if (cudaMemcpy(t->layers, dev_layers, sizeof(t->layers), cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemcpy(t->fused, dev_fused, sizeof(t->fused), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        set_error("reading the layer tables failed");
+        t->dev_layers = nullptr;
+        return nullptr;
+    }
+    return t;
+}
+
+}  // namespace q35
+
+extern "C" int qwen35_b200_prefill_bf16(const Qwen35PrefillArgs* in, qwen35_stream_t stream) {
+    using namespace q35;
+    if (!in) { set_error("null args"); return QWEN35_ERR_BAD_ARG; }
+    if (in->seq_len <= 0 || in->seq_len > in->max_seq_len || in->seq_len > ATT_PF_MAX_S) {
+        set_error("seq_len %d out of range (max_seq_len %d, library limit %d)", in->seq_len, in->max_seq_len, ATT_PF_MAX_S);
+        return QWEN35_ERR_BAD_ARG;
+    }
+    if (!in->token_ids || !in->embed_weight || !in->layer_weights || !in->fused_layer_weights || !in->hidden || !in->proj_buf) {
+        set_error("null tensor pointer");
+        return QWEN35_ERR_BAD_ARG;
+    }
+    const HostTables* t = host_tables(in->layer_weights, in->fused_layer_weights);
+    if (!t) return QWEN35_ERR_CUDA;
+    PrefillArgs a = {};
+    a.token_ids = in->token_ids; a.S = in->seq_len; a.out_token = in->out_token;
+    a.embed = (const bf16*)in->embed_weight; a.layers_host = t->layers; a.fused_host = t->fused;
+    a.final_norm = (const bf16*)in->final_norm_weight; a.lm_head = (const bf16*)in->lm_head_weight;
+    a.k_cache = (bf16*)in->fa_k_cache; a.v_cache = (bf16*)in->fa_v_cache; a.dn_states = (float*)in->dn_states; a.conv_bufs = (float*)in->conv_bufs;
+    a.hidden = (bf16*)in->hidden; a.residual = (bf16*)in->residual; a.normalized = (bf16*)in->normalized;
+    a.proj_buf = (bf16*)in->proj_buf; a.proj_buf2 = (bf16*)in->proj_buf2; a.attn_buf = (bf16*)in->attn_buf; a.mlp_buf = (bf16*)in->mlp_buf;
+    a.dn_out_buf = (bf16*)in->dn_out_buf; a.beta_buf = (float*)in->beta_buf; a.alpha_buf = (float*)in->alpha_buf;
+    a.final_normed = (bf16*)in->final_normed; a.hidden_out = (bf16*)in->hidden_bf16_out;
+    a.lm_bmv = (float*)in->lm_bmv; a.lm_bmi = (int*)in->lm_bmi; a.logits_out = in->logits_out;
+    a.max_seq_len = in->max_seq_len;
+    a.n_layers = in->dbg_num_layers > 0 ? in->dbg_num_layers : NUM_LAYERS;
+    return prefill_impl(a, (cudaStream_t)stream);
+}
+
+extern "C" int launch_prefill_bf16(
+    const int* token_ids, int seq_len, int* output_token,
+    const void* embed_weight, const LayerWeights* layers, const void* fused_layers,
+    const void* final_norm_w, const void* lm_head_w,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* hidden, void* residual, void* normalized,
+    void* proj_buf, void* proj_buf2, void* /*proj_buf_half*/, void* /*proj_act_packed*/, void* /*proj_act_scales*/,
+    void* attn_buf, void* mlp_buf, void* dn_out_buf, void* beta_buf, void* alpha_buf,
+    void* final_normed, void* hidden_bf16_out, void* lm_bmv, void* lm_bmi, qwen35_stream_t stream) {
+    Qwen35PrefillArgs a = {};
+    a.token_ids = token_ids; a.seq_len = seq_len; a.out_token = output_token;
+    a.embed_weight = embed_weight; a.layer_weights = layers; a.fused_layer_weights = fused_layers;
+    a.final_norm_weight = final_norm_w; a.lm_head_weight = lm_head_w;
+    a.fa_k_cache = fa_k_cache; a.fa_v_cache = fa_v_cache; a.dn_states = dn_states; a.conv_bufs = conv_bufs;
+    a.hidden = hidden; a.residual = residual; a.normalized = normalized; a.proj_buf = proj_buf; a.proj_buf2 = proj_buf2;
+    a.attn_buf = attn_buf; a.mlp_buf = mlp_buf; a.dn_out_buf = dn_out_buf; a.beta_buf = beta_buf; a.alpha_buf = alpha_buf;
+    a.final_normed = final_normed; a.hidden_bf16_out = hidden_bf16_out; a.lm_bmv = lm_bmv; a.lm_bmi = lm_bmi;
+    a.max_seq_len = 2048;       // the reference's fixed cache length (prefill.cu:1203, 1394)
+    return qwen35_b200_prefill_bf16(&a, stream);
+}

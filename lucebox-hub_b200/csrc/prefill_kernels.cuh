@@ -1,0 +1,486 @@
+// Prefill kernels of the Qwen3.5-0.8B hybrid network other than the tensor-core GEMMs:
+// row norms, DeltaNet preparation (causal conv + SiLU + L2 norm, beta / log-decay), the chunk-64
+// gated delta rule in two kernels (chunk-local triangular solve, then the scan over chunks),
+// gated norm, q/k norm + RoPE + KV-cache fill, causal GQA attention and the last-token LM head.
+//
+// These replace pf_embed / pf_rmsnorm / pf_deltanet_prepare_qk / pf_deltanet_recurrence_tiled /
+// pf_deltanet_finalize / pf_qk_norm_rope / pf_causal_attn_posblock / pf_lm_head of the reference
+// (models/qwen35_0p8b/prefill.cu:118-892).  The reference runs the delta rule token by token
+// (:385-544, 85 % of its prefill time); here it is the chunked (WY) form with all products in f32.
+// Rounding points follow a bf16 HuggingFace model: every module output is rounded to bf16 once.
+#pragma once
+
+#include "common.cuh"
+
+namespace q35 {
+
+constexpr int DN_CHUNK = 64;
+
+// ---- one CTA (128 threads) per token: optional embedding gather, RMSNorm(1+w) -------------------
+// h_out (may be null) receives the raw row; x_out the normalised row.
+__global__ void __launch_bounds__(128) pf_rmsnorm_kernel(const int* __restrict__ ids, const bf16* __restrict__ embed,
+                                                         const bf16* __restrict__ h_in, const bf16* __restrict__ w,
+                                                         bf16* __restrict__ h_out, bf16* __restrict__ x_out, int S) {
+    __shared__ float red[4];
+    const int t = blockIdx.x, tid = threadIdx.x;
+    const bf16* src = ids ? embed + (size_t)ids[t] * HIDDEN : h_in + (size_t)t * HIDDEN;
+    const uint4 raw = *(reinterpret_cast<const uint4*>(src) + tid);
+    if (h_out) *(reinterpret_cast<uint4*>(h_out + (size_t)t * HIDDEN) + tid) = raw;
+    float x[8];
+    x[0] = bf_lo(raw.x); x[1] = bf_hi(raw.x); x[2] = bf_lo(raw.y); x[3] = bf_hi(raw.y);
+    x[4] = bf_lo(raw.z); x[5] = bf_hi(raw.z); x[6] = bf_lo(raw.w); x[7] = bf_hi(raw.w);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    const float tot = (red[0] + red[1]) + (red[2] + red[3]);
+    const float r = rsqrt_ieee(tot * (1.0f / HIDDEN) + RMS_EPS);
+    const uint4 wr = __ldg(reinterpret_cast<const uint4*>(w) + tid);
+    const float wv[8] = {bf_lo(wr.x), bf_hi(wr.x), bf_lo(wr.y), bf_hi(wr.y), bf_lo(wr.z), bf_hi(wr.z), bf_lo(wr.w), bf_hi(wr.w)};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat162 p = __halves2bfloat162(f2bf((x[2 * i] * r) * (1.0f + wv[2 * i])), f2bf((x[2 * i + 1] * r) * (1.0f + wv[2 * i + 1])));
+        o[i] = *reinterpret_cast<const uint32_t*>(&p);
+    }
+    *(reinterpret_cast<uint4*>(x_out + (size_t)t * HIDDEN) + tid) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// ---- DeltaNet preparation: one CTA (128 threads) per (token, head) -----------------------------------
+// proj: [S, ldp] bf16 rows [qkv 6144 | z 2048 | b 16 | a 16].  Writes qkv_out [S, 6144] bf16 (q, k L2-normalised
+// in bf16 arithmetic, v after conv + SiLU), beta [S,16] (bf16-rounded sigmoid), g [S,16] (f32 log-decay).
+__global__ void __launch_bounds__(128) pf_dn_prep_kernel(const bf16* __restrict__ proj, int ldp, const bf16* __restrict__ conv_w,
+                                                         const bf16* __restrict__ a_log, const bf16* __restrict__ dt_bias,
+                                                         bf16* __restrict__ qkv_out, float* __restrict__ beta, float* __restrict__ g, int S) {
+    __shared__ float red[2][4];
+    const int t = blockIdx.x, h = blockIdx.y, i = threadIdx.x;
+    float c[3];
+#pragma unroll
+    for (int part = 0; part < 3; ++part) {
+        const int ch = part * DN_QK_SIZE + h * DN_K + i;
+        const uint2 wr = __ldg(reinterpret_cast<const uint2*>(conv_w) + ch);
+        const float w4[4] = {bf_lo(wr.x), bf_hi(wr.x), bf_lo(wr.y), bf_hi(wr.y)};
+        float acc = 0.f;
+        bool first = true;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int tt = t - 3 + j;
+            const float xv = (tt >= 0) ? bf2f(proj[(size_t)tt * ldp + ch]) : 0.f;
+            acc = first ? w4[j] * xv : fmaf(w4[j], xv, acc);
+            first = false;
+        }
+        c[part] = rbf(silu_f(rbf(acc)));
+    }
+    // L2 norm of q and k in bf16 arithmetic: squares rounded, f32 sum rounded once, + eps, rsqrt, scale.
+    const float sq0 = warp_sum(rbf(c[0] * c[0])), sq1 = warp_sum(rbf(c[1] * c[1]));
+    if ((i & 31) == 0) { red[0][i >> 5] = sq0; red[1][i >> 5] = sq1; }
+    __syncthreads();
+    // torch's vectorised CPU rsqrt rounds once; its scalar tail (the last S*16 mod 32 elements, i.e. the last
+    // token when S is odd) rounds sqrt to bf16 first.  The oracle is that CPU path, so both are mirrored.
+    const bool scalar_tail = (S & 1) && (t == S - 1);
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+        float tot = ((red[part][0] + red[part][1]) + red[part][2]) + red[part][3];
+        tot = rbf(rbf(tot) + 1e-6f);
+        const float inv = scalar_tail ? rbf(1.0f / rbf(sqrtf(tot))) : rbf(rsqrt_ieee(tot));
+        c[part] = rbf(c[part] * inv);
+    }
+    bf16* dst = qkv_out + (size_t)t * DN_CONV_CH + h * DN_K + i;
+    dst[0] = f2bf(c[0]);
+    dst[DN_QK_SIZE] = f2bf(c[1]);
+    dst[2 * DN_QK_SIZE] = f2bf(c[2]);
+    if (i == 0) {
+        const float bb = bf2f(proj[(size_t)t * ldp + DN_CONV_CH + DN_V_SIZE + h]);
+        const float aa = bf2f(proj[(size_t)t * ldp + DN_CONV_CH + DN_V_SIZE + DN_HEADS + h]);
+        beta[t * DN_HEADS + h] = rbf(sigmoid_f(bb));
+        const float x = aa + bf2f(dt_bias[h]);
+        const float sp = (x > 20.f) ? x : log1pf(expf(x));
+        g[t * DN_HEADS + h] = -expf(bf2f(a_log[h])) * sp;
+    }
+}
+
+// conv window after the prompt: the last four inputs per channel, zero-padded on the left, newest last
+__global__ void pf_conv_state_kernel(const bf16* __restrict__ proj, int ldp, float* __restrict__ conv, int S) {
+    const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+    if (ch >= DN_CONV_CH) return;
+    float4 st;
+    float* sv = reinterpret_cast<float*>(&st);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int tt = S - 4 + j;
+        sv[j] = (tt >= 0) ? bf2f(proj[(size_t)tt * ldp + ch]) : 0.f;
+    }
+    reinterpret_cast<float4*>(conv)[ch] = st;
+}
+
+// ---- chunk-local part of the gated delta rule: one CTA (256 threads) per (chunk, head) --------------
+// Per chunk of 64 tokens (zero padded): gc = cumsum(g); T = (I + tril(-(k beta) k^T * decay, -1))^-1 by forward
+// substitution; vprime = T (v beta); kcd = T (k beta exp(gc)); aqk = tril(q k^T * decay).  All f32.
+struct ChunkScratch {          // one record per (head, chunk), floats
+    float vprime[DN_CHUNK][DN_V];
+    float kcd[DN_CHUNK][DN_K];
+    float aqk[DN_CHUNK][DN_CHUNK];
+    float gc[DN_CHUNK];
+};
+
+constexpr int CHUNK_LOCAL_SMEM = (2 * DN_CHUNK * (DN_K + 1) + DN_CHUNK * DN_V + DN_CHUNK * (DN_CHUNK + 1) + 3 * DN_CHUNK) * 4;
+
+__global__ void __launch_bounds__(256) pf_dn_chunk_local_kernel(const bf16* __restrict__ qkv, const float* __restrict__ beta,
+                                                                const float* __restrict__ g, ChunkScratch* __restrict__ scratch,
+                                                                int S, int nchunks) {
+    extern __shared__ float sm[];
+    float (*sq)[DN_K + 1] = reinterpret_cast<float (*)[DN_K + 1]>(sm);                       // q * 1/sqrt(128)
+    float (*sk)[DN_K + 1] = reinterpret_cast<float (*)[DN_K + 1]>(sm + DN_CHUNK * (DN_K + 1));
+    float (*sv)[DN_V] = reinterpret_cast<float (*)[DN_V]>(sm + 2 * DN_CHUNK * (DN_K + 1));     // v * beta
+    float (*sa)[DN_CHUNK + 1] = reinterpret_cast<float (*)[DN_CHUNK + 1]>(sm + 2 * DN_CHUNK * (DN_K + 1) + DN_CHUNK * DN_V);
+    float* sb = sm + 2 * DN_CHUNK * (DN_K + 1) + DN_CHUNK * DN_V + DN_CHUNK * (DN_CHUNK + 1);
+    float* sg = sb + DN_CHUNK;      // cumulative log-decay
+    float* se = sg + DN_CHUNK;      // exp(gc)
+    const int c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    const int t0 = c * DN_CHUNK;
+    ChunkScratch& out = scratch[(size_t)h * nchunks + c];
+
+    if (tid < DN_CHUNK) {
+        const int t = t0 + tid;
+        sb[tid] = (t < S) ? beta[t * DN_HEADS + h] : 0.f;
+        sg[tid] = (t < S) ? g[t * DN_HEADS + h] : 0.f;
+    }
+    for (int e = tid; e < DN_CHUNK * DN_K; e += 256) {
+        const int i = e >> 7, d = e & 127, t = t0 + i;
+        float qv = 0.f, kv = 0.f, vv = 0.f;
+        if (t < S) {
+            const bf16* row = qkv + (size_t)t * DN_CONV_CH + h * DN_K + d;
+            qv = bf2f(row[0]) * 0.08838834764831845f;
+            kv = bf2f(row[DN_QK_SIZE]);
+            vv = bf2f(row[2 * DN_QK_SIZE]);
+        }
+        sq[i][d] = qv; sk[i][d] = kv; sv[i][d] = vv;
+    }
+    __syncthreads();
+    if (tid == 0) {                 // sequential cumsum, as torch.cumsum does
+        float acc = 0.f;
+        for (int i = 0; i < DN_CHUNK; ++i) { acc += sg[i]; sg[i] = acc; }
+    }
+    __syncthreads();
+    if (tid < DN_CHUNK) { se[tid] = expf(sg[tid]); out.gc[tid] = sg[tid]; }
+    for (int e = tid; e < DN_CHUNK * DN_V; e += 256) sv[e >> 7][e & 127] *= sb[e >> 7];      // v * beta
+    __syncthreads();
+    // A[i][j] = -(beta_i k_i . k_j) * exp(gc_i - gc_j) for j < i, else 0;   aqk[i][j] = (q_i . k_j) * exp(gc_i - gc_j) for j <= i
+    for (int e = tid; e < DN_CHUNK * DN_CHUNK; e += 256) {
+        const int i = e >> 6, j = e & 63;
+        float kk = 0.f, qk = 0.f;
+        if (j <= i) {
+            for (int d = 0; d < DN_K; ++d) { kk = fmaf(sk[i][d] * sb[i], sk[j][d], kk); qk = fmaf(sq[i][d], sk[j][d], qk); }
+        }
+        const float dec = (j <= i) ? expf(sg[i] - sg[j]) : 0.f;
+        sa[i][j] = (j < i) ? -(kk * dec) : 0.f;
+        out.aqk[i][j] = (j <= i) ? qk * dec : 0.f;
+    }
+    __syncthreads();
+    // forward substitution, row by row: row_i[:i] += sum_{j<i} row_i[j] * A[j][:i]  (rows j < i already final)
+    for (int i = 1; i < DN_CHUNK; ++i) {
+        float nv = 0.f;
+        if (tid < i) {
+            float acc = 0.f;
+            for (int j = 0; j < i; ++j) acc += sa[i][j] * sa[j][tid];
+            nv = sa[i][tid] + acc;
+        }
+        __syncthreads();
+        if (tid < i) sa[i][tid] = nv;
+        __syncthreads();
+    }
+    if (tid < DN_CHUNK) sa[tid][tid] = 1.0f;
+    __syncthreads();
+    // vprime = T (v beta);  kcd = T (k beta exp(gc))
+    for (int e = tid; e < DN_CHUNK * DN_V; e += 256) {
+        const int i = e >> 7, d = e & 127;
+        float a0 = 0.f, a1 = 0.f;
+        for (int j = 0; j <= i; ++j) {
+            const float tv = sa[i][j];
+            a0 = fmaf(tv, sv[j][d], a0);
+            a1 = fmaf(tv, (sk[j][d] * sb[j]) * se[j], a1);
+        }
+        out.vprime[i][d] = a0;
+        out.kcd[i][d] = a1;
+    }
+}
+
+// ---- scan over chunks: one CTA (256 threads) per (head, 16-wide slice of the value dimension) --------
+constexpr int SCAN_VW = 16;
+constexpr int CHUNK_SCAN_SMEM = (3 * DN_CHUNK * (DN_K + 1) + DN_CHUNK * (DN_CHUNK + 1) + 2 * DN_CHUNK * SCAN_VW + DN_K * SCAN_VW + 2 * DN_CHUNK) * 4;
+
+__global__ void __launch_bounds__(256) pf_dn_chunk_scan_kernel(const bf16* __restrict__ qkv, const ChunkScratch* __restrict__ scratch,
+                                                               bf16* __restrict__ core_out, float* __restrict__ state_out,
+                                                               int S, int nchunks) {
+    extern __shared__ float sm[];
+    float (*skcd)[DN_K + 1] = reinterpret_cast<float (*)[DN_K + 1]>(sm);
+    float (*sq)[DN_K + 1] = reinterpret_cast<float (*)[DN_K + 1]>(sm + DN_CHUNK * (DN_K + 1));      // q * scale * exp(gc_i)
+    float (*sk)[DN_K + 1] = reinterpret_cast<float (*)[DN_K + 1]>(sm + 2 * DN_CHUNK * (DN_K + 1));  // k * exp(gc_last - gc_i)
+    float (*sa)[DN_CHUNK + 1] = reinterpret_cast<float (*)[DN_CHUNK + 1]>(sm + 3 * DN_CHUNK * (DN_K + 1));
+    float (*svp)[SCAN_VW] = reinterpret_cast<float (*)[SCAN_VW]>(sm + 3 * DN_CHUNK * (DN_K + 1) + DN_CHUNK * (DN_CHUNK + 1));
+    float (*svn)[SCAN_VW] = svp + DN_CHUNK;
+    float (*sst)[SCAN_VW] = svn + DN_CHUNK;                    // state slice [k][v]
+    float* sgc = reinterpret_cast<float*>(sst + DN_K);
+    float* seg = sgc + DN_CHUNK;
+    const int h = blockIdx.x, vs = blockIdx.y, tid = threadIdx.x;
+    const int v0 = vs * SCAN_VW;
+    for (int e = tid; e < DN_K * SCAN_VW; e += 256) sst[e / SCAN_VW][e % SCAN_VW] = 0.f;
+
+    for (int c = 0; c < nchunks; ++c) {
+        const ChunkScratch& in = scratch[(size_t)h * nchunks + c];
+        const int t0 = c * DN_CHUNK;
+        __syncthreads();
+        if (tid < DN_CHUNK) { sgc[tid] = in.gc[tid]; seg[tid] = expf(in.gc[tid]); }
+        __syncthreads();
+        const float g_last = sgc[DN_CHUNK - 1];
+        for (int e = tid; e < DN_CHUNK * DN_K; e += 256) {
+            const int i = e >> 7, d = e & 127, t = t0 + i;
+            float qv = 0.f, kv = 0.f;
+            if (t < S) {
+                const bf16* row = qkv + (size_t)t * DN_CONV_CH + h * DN_K + d;
+                qv = bf2f(row[0]) * 0.08838834764831845f;
+                kv = bf2f(row[DN_QK_SIZE]);
+            }
+            skcd[i][d] = in.kcd[i][d];
+            sq[i][d] = qv * seg[i];
+            sk[i][d] = kv * expf(g_last - sgc[i]);
+        }
+        for (int e = tid; e < DN_CHUNK * DN_CHUNK; e += 256) sa[e >> 6][e & 63] = in.aqk[e >> 6][e & 63];
+        for (int e = tid; e < DN_CHUNK * SCAN_VW; e += 256) svp[e / SCAN_VW][e % SCAN_VW] = in.vprime[e / SCAN_VW][v0 + e % SCAN_VW];
+        __syncthreads();
+        // v_new = vprime - kcd @ S ;  inter = (q exp gc) @ S      thread: row i = tid / 4, four value columns
+        const int i = tid >> 2, vq = (tid & 3) * 4;
+        float vp[4] = {0.f, 0.f, 0.f, 0.f}, it[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int d = 0; d < DN_K; ++d) {
+            const float4 s4 = *reinterpret_cast<const float4*>(&sst[d][vq]);
+            const float a = skcd[i][d], b = sq[i][d];
+            vp[0] = fmaf(a, s4.x, vp[0]); vp[1] = fmaf(a, s4.y, vp[1]); vp[2] = fmaf(a, s4.z, vp[2]); vp[3] = fmaf(a, s4.w, vp[3]);
+            it[0] = fmaf(b, s4.x, it[0]); it[1] = fmaf(b, s4.y, it[1]); it[2] = fmaf(b, s4.z, it[2]); it[3] = fmaf(b, s4.w, it[3]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) svn[i][vq + u] = svp[i][vq + u] - vp[u];
+        __syncthreads();
+        // out = inter + aqk @ v_new
+        {
+            float o[4] = {it[0], it[1], it[2], it[3]};
+            for (int j = 0; j <= i; ++j) {
+                const float a = sa[i][j];
+                const float4 n4 = *reinterpret_cast<const float4*>(&svn[j][vq]);
+                o[0] = fmaf(a, n4.x, o[0]); o[1] = fmaf(a, n4.y, o[1]); o[2] = fmaf(a, n4.z, o[2]); o[3] = fmaf(a, n4.w, o[3]);
+            }
+            const int t = t0 + i;
+            if (t < S) {
+                bf16* dst = core_out + (size_t)t * DN_V_SIZE + h * DN_V + v0 + vq;
+                *reinterpret_cast<__nv_bfloat162*>(dst) = __halves2bfloat162(f2bf(o[0]), f2bf(o[1]));
+                *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __halves2bfloat162(f2bf(o[2]), f2bf(o[3]));
+            }
+        }
+        // S = S * exp(g_last) + (k exp(g_last - gc))^T @ v_new       thread: key d = tid / 2, eight value columns
+        {
+            const int d = tid >> 1, vo = (tid & 1) * 8;
+            float acc[8];
+            const float dec = expf(g_last);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) acc[u] = sst[d][vo + u] * dec;
+            for (int j = 0; j < DN_CHUNK; ++j) {
+                const float kw = sk[j][d];
+                const float4 n0 = *reinterpret_cast<const float4*>(&svn[j][vo]);
+                const float4 n1 = *reinterpret_cast<const float4*>(&svn[j][vo + 4]);
+                acc[0] = fmaf(kw, n0.x, acc[0]); acc[1] = fmaf(kw, n0.y, acc[1]); acc[2] = fmaf(kw, n0.z, acc[2]); acc[3] = fmaf(kw, n0.w, acc[3]);
+                acc[4] = fmaf(kw, n1.x, acc[4]); acc[5] = fmaf(kw, n1.y, acc[5]); acc[6] = fmaf(kw, n1.z, acc[6]); acc[7] = fmaf(kw, n1.w, acc[7]);
+            }
+            __syncthreads();       // everyone has finished reading the old state
+#pragma unroll
+            for (int u = 0; u < 8; ++u) sst[d][vo + u] = acc[u];
+        }
+    }
+    __syncthreads();
+    // final state in the reference layout [head][v][k]
+    for (int e = tid; e < DN_K * SCAN_VW; e += 256) {
+        const int v = e / DN_K, d = e % DN_K;
+        state_out[((size_t)h * DN_V + v0 + v) * DN_K + d] = sst[d][v];
+    }
+}
+
+// ---- gated RMSNorm of the DeltaNet output: one warp per (token, head) --------------------------------
+__global__ void __launch_bounds__(256) pf_gated_norm_kernel(const bf16* __restrict__ core, const bf16* __restrict__ proj, int ldp,
+                                                            const bf16* __restrict__ norm_w, bf16* __restrict__ out, int S) {
+    const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (gw >= S * DN_HEADS) return;
+    const int t = gw / DN_HEADS, h = gw % DN_HEADS;
+    const uint2 orw = *(reinterpret_cast<const uint2*>(core + (size_t)t * DN_V_SIZE + h * DN_V) + lane);
+    const uint2 zrw = *(reinterpret_cast<const uint2*>(proj + (size_t)t * ldp + DN_CONV_CH + h * DN_V) + lane);
+    const uint2 nrw = __ldg(reinterpret_cast<const uint2*>(norm_w) + lane);
+    const float ov[4] = {bf_lo(orw.x), bf_hi(orw.x), bf_lo(orw.y), bf_hi(orw.y)};
+    const float zv[4] = {bf_lo(zrw.x), bf_hi(zrw.x), bf_lo(zrw.y), bf_hi(zrw.y)};
+    const float nw[4] = {bf_lo(nrw.x), bf_hi(nrw.x), bf_lo(nrw.y), bf_hi(nrw.y)};
+    const float var = warp_sum(ov[0] * ov[0] + ov[1] * ov[1] + ov[2] * ov[2] + ov[3] * ov[3]) * (1.0f / DN_V);
+    const float r = rsqrt_ieee(var + RMS_EPS);
+    float u[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) u[i] = rbf(nw[i] * rbf(ov[i] * r)) * silu_f(zv[i]);
+    bf16* dst = out + (size_t)t * DN_V_SIZE + h * DN_V + lane * 4;
+    *reinterpret_cast<__nv_bfloat162*>(dst) = __halves2bfloat162(f2bf(u[0]), f2bf(u[1]));
+    *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __halves2bfloat162(f2bf(u[2]), f2bf(u[3]));
+}
+
+// ---- attention preparation: one warp per (token, head slot); slots 0-7 query heads, 8-9 key heads, 10-11 value heads
+// proj rows: [per head q(256) | gate(256)] x 8, k 512, v 512.  q -> q_out [S, 2048]; k, v -> cache rows [kv_head][t][256].
+struct RopeTable { float f[FA_ROT / 2]; };
+
+__global__ void __launch_bounds__(256) pf_qk_norm_rope_kernel(const bf16* __restrict__ proj, int ldp, const bf16* __restrict__ qn_w,
+                                                              const bf16* __restrict__ kn_w, const RopeTable inv_freq,
+                                                              bf16* __restrict__ q_out, bf16* __restrict__ k_cache, bf16* __restrict__ v_cache,
+                                                              int S, int max_seq) {
+    const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (gw >= S * 12) return;
+    const int t = gw / 12, slot = gw % 12;
+    if (slot >= 10) {
+        const int kvh = slot - 10;
+        const uint4 v = *(reinterpret_cast<const uint4*>(proj + (size_t)t * ldp + FA_QPROJ + FA_KV_SIZE + kvh * FA_HEAD_DIM) + lane);
+        *(reinterpret_cast<uint4*>(v_cache + ((size_t)kvh * max_seq + t) * FA_HEAD_DIM) + lane) = v;
+        return;
+    }
+    const bool isq = slot < 8;
+    const bf16* src = proj + (size_t)t * ldp + (isq ? slot * 2 * FA_HEAD_DIM : FA_QPROJ + (slot - 8) * FA_HEAD_DIM);
+    const bf16* nw = isq ? qn_w : kn_w;
+    float xv[8], ss = 0.f;       // xv[i] = element lane + 32 i
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { xv[i] = bf2f(src[lane + 32 * i]); ss += xv[i] * xv[i]; }
+    const float r = rsqrt_ieee(warp_sum(ss) * (1.0f / FA_HEAD_DIM) + RMS_EPS);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xv[i] = rbf((xv[i] * r) * (1.0f + bf2f(nw[lane + 32 * i])));
+    const float ang = (float)t * inv_freq.f[lane];
+    const float cs = rbf(cosf(ang)), sn = rbf(sinf(ang));
+    const float x1 = xv[0], x2 = xv[1];
+    xv[0] = rbf(rbf(x1 * cs) + rbf(-x2 * sn));
+    xv[1] = rbf(rbf(x2 * cs) + rbf(x1 * sn));
+    bf16* dst = isq ? q_out + (size_t)t * FA_Q_SIZE + slot * FA_HEAD_DIM : k_cache + ((size_t)(slot - 8) * max_seq + t) * FA_HEAD_DIM;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dst[lane + 32 * i] = f2bf(xv[i]);
+}
+
+// ---- causal GQA attention, exact bf16 rounding points: one warp per (query, head) ----------------------
+// scores = bf16(q.k)/16, softmax in f32 over the whole row, P rounded to bf16, out = bf16(P.V), times bf16(sigmoid(gate)).
+// The row of scores lives in shared memory (S <= ATT_PF_MAX_S).
+constexpr int ATT_PF_MAX_S = 4096;
+constexpr int ATT_PF_WARPS = 8;
+
+__global__ void __launch_bounds__(ATT_PF_WARPS * 32) pf_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k_cache,
+                                                                         const bf16* __restrict__ v_cache, const bf16* __restrict__ proj, int ldp,
+                                                                         bf16* __restrict__ out, int S, int max_seq) {
+    extern __shared__ float att_sm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int head = blockIdx.y, kvh = head / FA_GQA;
+    const int t = (int)gridDim.x * ATT_PF_WARPS - 1 - (blockIdx.x * ATT_PF_WARPS + warp);      // long rows first
+    float* sc = att_sm + (size_t)warp * S;
+    float* sqv = att_sm + (size_t)ATT_PF_WARPS * S + warp * FA_HEAD_DIM;
+    if (t >= S || t < 0) return;
+    for (int i = lane; i < FA_HEAD_DIM; i += 32) sqv[i] = bf2f(q[(size_t)t * FA_Q_SIZE + head * FA_HEAD_DIM + i]);
+    __syncwarp();
+    const bf16* kb = k_cache + (size_t)kvh * max_seq * FA_HEAD_DIM;
+    const bf16* vb = v_cache + (size_t)kvh * max_seq * FA_HEAD_DIM;
+    const int L = t + 1;
+    // pass 1: one key per lane
+    float mx = -INFINITY;
+    for (int j = lane; j < L; j += 32) {
+        const uint4* kr = reinterpret_cast<const uint4*>(kb + (size_t)j * FA_HEAD_DIM);
+        float d = 0.f;
+#pragma unroll 4
+        for (int cidx = 0; cidx < FA_HEAD_DIM / 8; ++cidx) {
+            const uint4 kv = kr[cidx];
+            const float* qq = sqv + cidx * 8;
+            d = fmaf(qq[0], bf_lo(kv.x), d); d = fmaf(qq[1], bf_hi(kv.x), d);
+            d = fmaf(qq[2], bf_lo(kv.y), d); d = fmaf(qq[3], bf_hi(kv.y), d);
+            d = fmaf(qq[4], bf_lo(kv.z), d); d = fmaf(qq[5], bf_hi(kv.z), d);
+            d = fmaf(qq[6], bf_lo(kv.w), d); d = fmaf(qq[7], bf_hi(kv.w), d);
+        }
+        const float s = rbf(d) * 0.0625f;
+        sc[j] = s;
+        mx = fmaxf(mx, s);
+    }
+    mx = warp_max(mx);
+    float sm = 0.f;
+    for (int j = lane; j < L; j += 32) sm += expf(sc[j] - mx);
+    sm = warp_sum(sm);
+    for (int j = lane; j < L; j += 32) sc[j] = rbf(expf(sc[j] - mx) / sm);
+    __syncwarp();
+    // pass 2: eight output dims per lane
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < L; ++j) {
+        const float p = sc[j];
+        const uint4 vv = *(reinterpret_cast<const uint4*>(vb + (size_t)j * FA_HEAD_DIM) + lane);
+        acc[0] = fmaf(p, bf_lo(vv.x), acc[0]); acc[1] = fmaf(p, bf_hi(vv.x), acc[1]);
+        acc[2] = fmaf(p, bf_lo(vv.y), acc[2]); acc[3] = fmaf(p, bf_hi(vv.y), acc[3]);
+        acc[4] = fmaf(p, bf_lo(vv.z), acc[4]); acc[5] = fmaf(p, bf_hi(vv.z), acc[5]);
+        acc[6] = fmaf(p, bf_lo(vv.w), acc[6]); acc[7] = fmaf(p, bf_hi(vv.w), acc[7]);
+    }
+    const uint4 gr = *(reinterpret_cast<const uint4*>(proj + (size_t)t * ldp + head * 2 * FA_HEAD_DIM + FA_HEAD_DIM) + lane);
+    const float gv[8] = {bf_lo(gr.x), bf_hi(gr.x), bf_lo(gr.y), bf_hi(gr.y), bf_lo(gr.z), bf_hi(gr.z), bf_lo(gr.w), bf_hi(gr.w)};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat162 pr = __halves2bfloat162(f2bf(rbf(acc[2 * i]) * rbf(sigmoid_f(gv[2 * i]))),
+                                                     f2bf(rbf(acc[2 * i + 1]) * rbf(sigmoid_f(gv[2 * i + 1]))));
+        o[i] = *reinterpret_cast<const uint32_t*>(&pr);
+    }
+    *(reinterpret_cast<uint4*>(out + (size_t)t * FA_Q_SIZE + head * FA_HEAD_DIM) + lane) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// ---- last-token LM head: GEMV over the vocabulary + arg-max (lowest index among equal bf16 maxima) -----
+__global__ void __launch_bounds__(256) pf_lm_head_kernel(const bf16* __restrict__ x, const bf16* __restrict__ lm, float* __restrict__ bmv,
+                                                         int* __restrict__ bmi, float* __restrict__ logits_out) {
+    __shared__ float sv[8];
+    __shared__ int si[8];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float xr[32];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint4 v = *(reinterpret_cast<const uint4*>(x) + j * 32 + lane);
+        xr[8 * j + 0] = bf_lo(v.x); xr[8 * j + 1] = bf_hi(v.x); xr[8 * j + 2] = bf_lo(v.y); xr[8 * j + 3] = bf_hi(v.y);
+        xr[8 * j + 4] = bf_lo(v.z); xr[8 * j + 5] = bf_hi(v.z); xr[8 * j + 6] = bf_lo(v.w); xr[8 * j + 7] = bf_hi(v.w);
+    }
+    const int r0 = part_begin(VOCAB, blockIdx.x, gridDim.x), r1 = part_begin(VOCAB, blockIdx.x + 1, gridDim.x);
+    float best = -INFINITY;
+    int best_i = 0x7fffffff;
+    for (int r = r0 + warp; r < r1; r += 8) {
+        const uint4* wr = reinterpret_cast<const uint4*>(lm + (size_t)r * HIDDEN) + lane;
+        float a = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint4 q = ld_stream(wr + j * 32);
+            a = fmaf(bf_lo(q.x), xr[8 * j + 0], a); a = fmaf(bf_hi(q.x), xr[8 * j + 1], a);
+            a = fmaf(bf_lo(q.y), xr[8 * j + 2], a); a = fmaf(bf_hi(q.y), xr[8 * j + 3], a);
+            a = fmaf(bf_lo(q.z), xr[8 * j + 4], a); a = fmaf(bf_hi(q.z), xr[8 * j + 5], a);
+            a = fmaf(bf_lo(q.w), xr[8 * j + 6], a); a = fmaf(bf_hi(q.w), xr[8 * j + 7], a);
+        }
+        const float v = rbf(warp_sum(a));
+        if (lane == 0 && logits_out) logits_out[r] = v;
+        if (v > best) { best = v; best_i = r; }
+    }
+    if (lane == 0) { sv[warp] = best; si[warp] = best_i; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float bv = sv[0]; int bi = si[0];
+        for (int w = 1; w < 8; ++w) if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+        bmv[blockIdx.x] = bv; bmi[blockIdx.x] = bi;
+    }
+}
+
+__global__ void pf_lm_reduce_kernel(const float* __restrict__ bmv, const int* __restrict__ bmi, int n, int* __restrict__ out_token) {
+    float bv = -INFINITY; int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += 32) {
+        const float v = bmv[i]; const int k = bmi[i];
+        if (v > bv || (v == bv && k < bi)) { bv = v; bi = k; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float v = __shfl_xor_sync(0xffffffffu, bv, o); const int k = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (v > bv || (v == bv && k < bi)) { bv = v; bi = k; }
+    }
+    if (threadIdx.x == 0) *out_token = bi;
+}
+
+}  // namespace q35

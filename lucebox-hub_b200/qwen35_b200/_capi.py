@@ -31,6 +31,20 @@ class DecodeArgs(C.Structure):
     ]
 
 
+class PrefillArgs(C.Structure):
+    _fields_ = [
+        ("token_ids", C.c_void_p), ("seq_len", C.c_int), ("out_token", C.c_void_p),
+        ("embed_weight", C.c_void_p), ("layer_weights", C.c_void_p), ("fused_layer_weights", C.c_void_p),
+        ("final_norm_weight", C.c_void_p), ("lm_head_weight", C.c_void_p),
+        ("fa_k_cache", C.c_void_p), ("fa_v_cache", C.c_void_p), ("dn_states", C.c_void_p), ("conv_bufs", C.c_void_p),
+        ("hidden", C.c_void_p), ("residual", C.c_void_p), ("normalized", C.c_void_p),
+        ("proj_buf", C.c_void_p), ("proj_buf2", C.c_void_p), ("attn_buf", C.c_void_p), ("mlp_buf", C.c_void_p),
+        ("dn_out_buf", C.c_void_p), ("beta_buf", C.c_void_p), ("alpha_buf", C.c_void_p),
+        ("final_normed", C.c_void_p), ("hidden_bf16_out", C.c_void_p), ("lm_bmv", C.c_void_p), ("lm_bmi", C.c_void_p),
+        ("logits_out", C.c_void_p), ("max_seq_len", C.c_int), ("dbg_num_layers", C.c_int),
+    ]
+
+
 _lib = None
 
 # name -> (restype, argtypes); every symbol include/qwen35_b200.h declares
@@ -38,6 +52,8 @@ _vp, _i = C.c_void_p, C.c_int
 SIGNATURES = {
     "launch_decode": (_i, [_i, _vp] + [_vp] * 8 + [_vp] * 11 + [_vp] * 5 + [_i, _i, _vp]),
     "qwen35_b200_decode_steps": (_i, [C.POINTER(DecodeArgs), _vp]),
+    "qwen35_b200_prefill_bf16": (_i, [C.POINTER(PrefillArgs), _vp]),
+    "launch_prefill_bf16": (_i, [_vp, _i, _vp] + [_vp] * 5 + [_vp] * 4 + [_vp] * 3 + [_vp] * 5 + [_vp] * 5 + [_vp] * 4 + [_vp]),
     "qwen35_b200_gemm_bf16": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "qwen35_b200_status": (_i, [_vp]),
     "qwen35_b200_clear_status": (_i, [_vp]),

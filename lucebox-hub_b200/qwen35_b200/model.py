@@ -55,6 +55,37 @@ def load_weights(model_name="random:1234", verbose=True, backend="bf16", device=
     return weights_to(w, device), None
 
 
+DN_PROJ_FUSED_SIZE = DN_CONV_CHANNELS + DN_V_SIZE + 2 * DN_NUM_HEADS
+DN_PROJ_FUSED_PADDED_SIZE = ((DN_PROJ_FUSED_SIZE + 127) // 128) * 128
+PREFILL_PROJ_FUSED_SIZE = max(DN_PROJ_FUSED_PADDED_SIZE, FA_QPROJ_SIZE + 2 * FA_KV_SIZE, INTERMEDIATE_SIZE * 2)
+PREFILL_PROJ_SCRATCH_SIZE = max(DN_CONV_CHANNELS, FA_QPROJ_SIZE, INTERMEDIATE_SIZE)
+
+
+def _attach_prefill_fused_weights(weights):
+    """Concatenated projection and gate/up matrices per layer (reference model.py:171-189)."""
+    if "prefill_fused_layer_data" in weights:
+        return
+    fused = []
+    for ld in weights["layer_data"]:
+        p = ld["ptrs"]
+        if ld["type"] == 1:
+            proj = torch.cat([p[1], p[2], p[3]], dim=0).contiguous()
+            gate_up = torch.cat([p[8], p[9]], dim=0).contiguous()
+        else:
+            proj = torch.cat([p[1], p[2], p[3], p[4]], dim=0).contiguous()
+            gate_up = torch.cat([p[11], p[12]], dim=0).contiguous()
+        fused.append({"proj_weight": proj, "gate_up_weight": gate_up})
+    weights["prefill_fused_layer_data"] = fused
+
+
+def _pack_prefill_fused_layer_weights(fused_layer_data, device="cuda"):
+    """Device blob of 6-pointer records (reference model.py:450-470); the four NVFP4 slots stay null."""
+    buf = bytearray(len(fused_layer_data) * 48)
+    for i, ld in enumerate(fused_layer_data):
+        struct.pack_into("QQQQQQ", buf, i * 48, ld["proj_weight"].data_ptr(), ld["gate_up_weight"].data_ptr(), 0, 0, 0, 0)
+    return torch.frombuffer(buf, dtype=torch.uint8).to(device)
+
+
 def _pack_layer_weights(layer_data, device="cuda"):
     """Device blob of 24 records {int type; int pad[3]; void* ptrs[14]} (model.py:410-427)."""
     ptr_size, max_ptrs, header = 8, 14, 16
@@ -91,6 +122,10 @@ class Decoder:
         self._final_norm_weight = weights["final_norm_weight"]
         self._lm_head_weight = weights["lm_head_weight"]
         self._layer_weights_packed = _pack_layer_weights(weights["layer_data"], device)
+        _attach_prefill_fused_weights(weights)
+        self._prefill_fused_weights_packed = _pack_prefill_fused_layer_weights(weights["prefill_fused_layer_data"], device)
+        self._prefill_buffers = None
+        self._prefill_buffer_tokens = 0
 
         dev = self.device
         n_fa = sum(1 for t in LAYER_TYPE if t == 1)
@@ -165,17 +200,61 @@ class Decoder:
         self._position += num_steps
         return out
 
-    def prefill_tokens(self, token_ids: torch.Tensor, logits_out=None) -> int:
-        """Reset, run the prompt, return the first generated token (model.py:745-799)."""
+    def _ensure_prefill_buffers(self, max_tokens: int):
+        """Scratch of the batched prefill, sizes of the reference (model.py:569-602)."""
+        if self._prefill_buffers is not None and self._prefill_buffer_tokens >= max_tokens:
+            return self._prefill_buffers
+        bf16 = dict(dtype=torch.bfloat16, device=self.device)
+        f32 = dict(dtype=torch.float32, device=self.device)
+        self._prefill_buffers = dict(
+            hidden=torch.empty(max_tokens * HIDDEN_SIZE, **bf16),
+            residual=torch.empty(max_tokens * HIDDEN_SIZE, **bf16),
+            normalized=torch.empty(max_tokens * HIDDEN_SIZE, **bf16),
+            proj_buf=torch.empty(max_tokens * PREFILL_PROJ_FUSED_SIZE, **bf16),
+            proj_buf2=torch.empty(max_tokens * PREFILL_PROJ_SCRATCH_SIZE, **bf16),
+            attn_buf=torch.empty(max_tokens * max(FA_Q_SIZE, FA_KV_SIZE), **bf16),
+            mlp_buf=torch.empty(max_tokens * INTERMEDIATE_SIZE, **bf16),
+            dn_out_buf=torch.empty(max_tokens * DN_V_SIZE, **bf16),
+            beta_buf=torch.empty(max_tokens * DN_NUM_HEADS, **f32),
+            alpha_buf=torch.empty(max_tokens * DN_NUM_HEADS, **f32),
+            final_normed=torch.empty(HIDDEN_SIZE, **bf16),
+            hidden_bf16_out=torch.empty(HIDDEN_SIZE, **bf16),
+            lm_bmv=torch.empty(1024, **f32),
+            lm_bmi=torch.empty(1024, dtype=torch.int32, device=self.device),
+        )
+        self._prefill_buffer_tokens = max_tokens
+        return self._prefill_buffers
+
+    def prefill_tokens(self, token_ids: torch.Tensor, logits_out=None, mode="batched", dbg_num_layers=0) -> int:
+        """Reset, run the prompt, return the first generated token (reference model.py:745-799).
+        mode="batched": tensor-core GEMMs + chunk-64 gated delta rule + causal attention (the
+        reference's prefill_bf16 op).  mode="serial": the decode megakernel token by token (the
+        reference's token-serial `prefill_megakernel`, kernel_gb10_nvfp4.cu:1659-1755)."""
         if token_ids.device.type != "cuda" or token_ids.dtype != torch.int32 or token_ids.dim() != 1:
             raise TypeError("token_ids must be a 1D CUDA int32 tensor")
         self.reset()
         n = int(token_ids.numel())
         if n == 0:
             raise ValueError("empty prompt")
-        a = self._args(forced_ids=token_ids.data_ptr(), n_steps=n, lm_last_only=1,
-                       logits_out=_capi.ptr(logits_out))
-        self._run(a)
+        if mode == "serial":
+            a = self._args(forced_ids=token_ids.data_ptr(), n_steps=n, lm_last_only=1, logits_out=_capi.ptr(logits_out))
+            self._run(a)
+        else:
+            b = self._ensure_prefill_buffers(n)
+            a = _capi.PrefillArgs()
+            a.token_ids = token_ids.data_ptr(); a.seq_len = n; a.out_token = self._out_token.data_ptr()
+            a.embed_weight = self._embed_weight.data_ptr(); a.layer_weights = self._layer_weights_packed.data_ptr()
+            a.fused_layer_weights = self._prefill_fused_weights_packed.data_ptr()
+            a.final_norm_weight = self._final_norm_weight.data_ptr(); a.lm_head_weight = self._lm_head_weight.data_ptr()
+            a.fa_k_cache = self._fa_k_cache.data_ptr(); a.fa_v_cache = self._fa_v_cache.data_ptr()
+            a.dn_states = self._dn_states.data_ptr(); a.conv_bufs = self._conv_bufs.data_ptr()
+            for k in ("hidden", "residual", "normalized", "proj_buf", "proj_buf2", "attn_buf", "mlp_buf", "dn_out_buf",
+                      "beta_buf", "alpha_buf", "final_normed", "hidden_bf16_out", "lm_bmv", "lm_bmi"):
+                setattr(a, k, b[k].data_ptr())
+            a.logits_out = _capi.ptr(logits_out); a.max_seq_len = self.max_seq_len; a.dbg_num_layers = dbg_num_layers
+            with torch.cuda.device(self.device):
+                _capi.check(self._lib.qwen35_b200_prefill_bf16(C.byref(a), self._stream()), "prefill_bf16")
+            self._hidden.copy_(b["hidden_bf16_out"])
         self._position = n
         return int(self._out_token.item())
 
