@@ -232,9 +232,9 @@ __global__ void __launch_bounds__(256) pf_dn_chunk_scan_kernel(const bf16* __res
         const ChunkScratch& in = scratch[(size_t)h * nchunks + c];
         const int t0 = c * DN_CHUNK;
         __syncthreads();
-        if (tid < DN_CHUNK) { sgc[tid] = in.gc[tid]; seg[tid] = expf(in.gc[tid]); }
+        const float g_last = in.gc[DN_CHUNK - 1];
+        if (tid < DN_CHUNK) { const float gv = in.gc[tid]; sgc[tid] = expf(g_last - gv); seg[tid] = expf(gv); }
         __syncthreads();
-        const float g_last = sgc[DN_CHUNK - 1];
         for (int e = tid; e < DN_CHUNK * DN_K; e += 256) {
             const int i = e >> 7, d = e & 127, t = t0 + i;
             float qv = 0.f, kv = 0.f;
@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(256) pf_dn_chunk_scan_kernel(const bf16* __res
             }
             skcd[i][d] = in.kcd[i][d];
             sq[i][d] = qv * seg[i];
-            sk[i][d] = kv * expf(g_last - sgc[i]);
+            sk[i][d] = kv * sgc[i];
         }
         for (int e = tid; e < DN_CHUNK * DN_CHUNK; e += 256) sa[e >> 6][e & 63] = in.aqk[e >> 6][e & 63];
         for (int e = tid; e < DN_CHUNK * SCAN_VW; e += 256) svp[e / SCAN_VW][e % SCAN_VW] = in.vprime[e / SCAN_VW][v0 + e % SCAN_VW];
