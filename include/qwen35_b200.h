@@ -141,6 +141,23 @@ int qwen35_b200_prefill_bf16(const Qwen35PrefillArgs* args, qwen35_stream_t stre
 int qwen35_b200_gemm_bf16(const void* A, int lda, const void* B, int b_rows, void* C, int ldc, const void* R, int ldr,
                           int M, int N, int K, int epilogue, int up_row_offset, qwen35_stream_t stream);
 
+/* No counterpart in the reference.  qwen35_b200_decode_steps for callers that must not allocate: an
+ * inference server that hands all device memory to its own pool at start-up (a later cudaMalloc inside a
+ * library can then fail or fragment the pool), or a latency-critical loop in which the device-wide
+ * synchronisation of cudaMalloc/cudaFree would stall other streams.  The megakernel's inter-stage scratch
+ * is a fixed array of sizeof(StreamWorkspace) (about 0.6 MB) compiled into the library image; every GPU
+ * that loads the library holds one copy until the process exits.  The entry point calls no cudaMalloc,
+ * cudaFree or other allocating routine.
+ *   - Limit: max_seq_len <= 32768 tokens (what the array is sized for); larger values are rejected with
+ *     QWEN35_ERR_BAD_ARG and a message naming the limit.  Inputs, caches and outputs are the caller's.
+ *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress with that
+ *     device current); make that first call before any stream capture.
+ *   - All calls on a device share the one array and it keeps what the previous call wrote.  Stale words
+ *     are harmless because every word carries a call-specific epoch; the library clears the array itself
+ *     when the 32-bit epoch wraps.  Two calls that overlap on the GPU (different streams) race on the
+ *     array: serialise them.  The sticky status word of this array is included in qwen35_b200_status(). */
+int qwen35_b200_decode_steps_static(const Qwen35DecodeArgs* args, qwen35_stream_t stream);
+
 /* Synchronises `stream`, then returns the sticky device status word of the current device
  * (QWEN35_OK, or the first error a kernel recorded).  qwen35_b200_clear_status() re-arms the
  * library after an error. */

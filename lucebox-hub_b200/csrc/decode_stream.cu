@@ -786,6 +786,13 @@ static int decode_grid() {
 
 static unsigned g_epoch[64] = {};
 
+// Scratch of qwen35_b200_decode_steps_static: lives in the module image, one copy on every device that
+// loads the library, for the life of the process.  In host code this name is only a handle for
+// cudaGetSymbolAddress -- it is not a device address and must never be handed to a kernel.
+static __device__ __align__(256) unsigned char g_static_scratch[sizeof(StreamWorkspace)];
+static StreamWorkspace* g_static_ptr[64] = {};
+static unsigned g_static_epoch[64] = {};
+
 static int tma_period() {
     static int v = -1;
     if (v < 0) {
@@ -796,7 +803,7 @@ static int tma_period() {
     return v;
 }
 
-static int launch_decode_impl(const DecodeArgs& in, cudaStream_t stream) {
+static int launch_decode_impl(const DecodeArgs& in, cudaStream_t stream, bool use_static = false) {
     static std::once_flag once[64];
     static bool ready[64] = {};
     int dev = 0;
@@ -833,17 +840,30 @@ static int launch_decode_impl(const DecodeArgs& in, cudaStream_t stream) {
         const int cap = (g / FA_KV_HEADS < ATT_MAX_CHUNKS ? g / FA_KV_HEADS : ATT_MAX_CHUNKS) * ATT_CHUNK_MAX;
         if (a.max_seq_len > cap) { set_error("max_seq_len %d exceeds %d on this device", a.max_seq_len, cap); return QWEN35_ERR_BAD_ARG; }
     }
-    a.ws = (StreamWorkspace*)get_workspace();
-    if (!a.ws) return QWEN35_ERR_CUDA;
-    // epochs tag every flagged word; they only ever grow.  On wrap-around the words are cleared.
-    const unsigned long long need = 32ull * (unsigned long long)a.n_steps + 64ull;
-    if ((unsigned long long)g_epoch[dev] + need >= 0xffffff00ull) {
-        Q35_CUDA_OK(cudaMemsetAsync((char*)a.ws + 256, 0, sizeof(StreamWorkspace) - 256, stream));
-        g_epoch[dev] = 0;
+    unsigned* epoch = use_static ? &g_static_epoch[dev] : &g_epoch[dev];
+    if (use_static) {
+        if (!g_static_ptr[dev]) {
+            // once per device, with that device current: resolve the device address of the file-scope array
+            void* p = nullptr;
+            Q35_CUDA_OK(cudaGetSymbolAddress(&p, g_static_scratch));
+            g_static_ptr[dev] = (StreamWorkspace*)p;
+            register_status_word((int*)p);
+        }
+        a.ws = g_static_ptr[dev];
+    } else {
+        a.ws = (StreamWorkspace*)get_workspace();
     }
-    a.epoch_base = g_epoch[dev];
+    if (!a.ws) return QWEN35_ERR_CUDA;
+    // epochs tag every flagged word; they only ever grow, so words left by earlier calls never match.
+    // On wrap-around the words are cleared (a memset, not an allocation).
+    const unsigned long long need = 32ull * (unsigned long long)a.n_steps + 64ull;
+    if ((unsigned long long)*epoch + need >= 0xffffff00ull) {
+        Q35_CUDA_OK(cudaMemsetAsync((char*)a.ws + 256, 0, sizeof(StreamWorkspace) - 256, stream));
+        *epoch = 0;
+    }
+    a.epoch_base = *epoch;
     a.tma_period = tma_period();
-    g_epoch[dev] += (unsigned)(32u * (unsigned)a.n_steps);
+    *epoch += (unsigned)(32u * (unsigned)a.n_steps);
     void* params[] = {(void*)&a};
     Q35_CUDA_OK(cudaLaunchCooperativeKernel((const void*)decode_stream_kernel, dim3(decode_grid()), dim3(STREAM_THREADS), params, sizeof(Smem), stream));
     g_launches.fetch_add(1);
@@ -880,7 +900,7 @@ extern "C" int launch_decode(
     return q35::launch_decode_impl(a, (cudaStream_t)stream);
 }
 
-extern "C" int qwen35_b200_decode_steps(const Qwen35DecodeArgs* in, qwen35_stream_t stream) {
+static int decode_steps_common(const Qwen35DecodeArgs* in, qwen35_stream_t stream, bool use_static) {
     if (!in) { q35::set_error("null args"); return QWEN35_ERR_BAD_ARG; }
     q35::DecodeArgs a = {};
     a.layers = reinterpret_cast<const q35::LayerRec*>(in->layer_weights);
@@ -907,7 +927,23 @@ extern "C" int qwen35_b200_decode_steps(const Qwen35DecodeArgs* in, qwen35_strea
     a.dbg_num_layers = in->dbg_num_layers;
     a.dbg_time = in->dbg_time;
     a.dbg_time_cta = in->dbg_time_cta;
-    return q35::launch_decode_impl(a, (cudaStream_t)stream);
+    return q35::launch_decode_impl(a, (cudaStream_t)stream, use_static);
+}
+
+extern "C" int qwen35_b200_decode_steps(const Qwen35DecodeArgs* in, qwen35_stream_t stream) {
+    return decode_steps_common(in, stream, false);
+}
+
+// Same kernel, same arguments, but the inter-stage scratch is the file-scope device array above instead of
+// the workspace the library allocates on first use: this entry point never calls cudaMalloc, cudaFree or any
+// other allocating routine.  Its first call on a device resolves the array's device address.
+extern "C" int qwen35_b200_decode_steps_static(const Qwen35DecodeArgs* in, qwen35_stream_t stream) {
+    if (in && in->max_seq_len > q35::MAX_CTX) {
+        q35::set_error("max_seq_len %d exceeds the %d-token limit of the static scratch (%zu bytes)", in->max_seq_len, q35::MAX_CTX,
+                       sizeof(q35::StreamWorkspace));
+        return QWEN35_ERR_BAD_ARG;
+    }
+    return decode_steps_common(in, stream, true);
 }
 
 // Debug: synchronise the device and decode one flagged-word vector of the workspace to bf16 on the host.

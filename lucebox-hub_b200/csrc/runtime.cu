@@ -42,6 +42,15 @@ void* get_workspace() {
     return g_ws[dev];
 }
 
+static int* g_extra_status[MAX_DEVICES] = {};
+
+void register_status_word(int* dev_ptr) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) return;
+    std::lock_guard<std::mutex> lk(g_mu);
+    g_extra_status[dev] = dev_ptr;
+}
+
 int device_sm_count() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) return 0;
@@ -57,7 +66,12 @@ extern "C" int qwen35_b200_status(qwen35_stream_t stream) {
     if (!ws) return QWEN35_ERR_CUDA;
     int err = 0;
     Q35_CUDA_OK(cudaMemcpyAsync(&err, ws, sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+    int dev = 0;
+    int err2 = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < MAX_DEVICES && g_extra_status[dev])
+        Q35_CUDA_OK(cudaMemcpyAsync(&err2, g_extra_status[dev], sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream));
     Q35_CUDA_OK(cudaStreamSynchronize((cudaStream_t)stream));
+    if (!err) err = err2;
     if (err) set_error("device status %d (%s)", err, err == 1 ? "a bounded device-side wait ran out" : "bad argument seen on device");
     return err;
 }
@@ -67,6 +81,9 @@ extern "C" int qwen35_b200_clear_status(qwen35_stream_t stream) {
     void* ws = get_workspace();
     if (!ws) return QWEN35_ERR_CUDA;
     Q35_CUDA_OK(cudaMemsetAsync(ws, 0, 256, (cudaStream_t)stream));
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < MAX_DEVICES && g_extra_status[dev])
+        Q35_CUDA_OK(cudaMemsetAsync(g_extra_status[dev], 0, sizeof(int), (cudaStream_t)stream));
     return QWEN35_OK;
 }
 

@@ -14,6 +14,8 @@ namespace q35 {
 // on failure.
 void* get_workspace();
 size_t workspace_bytes();      // defined next to the kernels that lay the workspace out
+// Additional device status words (first int of another scratch area) that qwen35_b200_status() must read too.
+void register_status_word(int* dev_ptr);
 
 int device_sm_count();
 void set_error(const char* fmt, ...);

@@ -52,6 +52,7 @@ _vp, _i = C.c_void_p, C.c_int
 SIGNATURES = {
     "launch_decode": (_i, [_i, _vp] + [_vp] * 8 + [_vp] * 11 + [_vp] * 5 + [_i, _i, _vp]),
     "qwen35_b200_decode_steps": (_i, [C.POINTER(DecodeArgs), _vp]),
+    "qwen35_b200_decode_steps_static": (_i, [C.POINTER(DecodeArgs), _vp]),
     "qwen35_b200_prefill_bf16": (_i, [C.POINTER(PrefillArgs), _vp]),
     "launch_prefill_bf16": (_i, [_vp, _i, _vp] + [_vp] * 5 + [_vp] * 4 + [_vp] * 3 + [_vp] * 5 + [_vp] * 5 + [_vp] * 4 + [_vp]),
     "qwen35_b200_gemm_bf16": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp]),
