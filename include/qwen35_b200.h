@@ -134,6 +134,18 @@ typedef struct {
 } Qwen35PrefillArgs;
 int qwen35_b200_prefill_bf16(const Qwen35PrefillArgs* args, qwen35_stream_t stream);
 
+/* Replaces launch_quantize_nvfp4_out (torch_bindings.cpp:79-81; kernel_gb10_nvfp4.cu:1757-1876): pack a bf16
+ * matrix [rows, cols] into the decode-body NVFP4 layout: packed uint8 [rows, cols/2] (low nibble = even
+ * element) and fp16 scales [rows, cols/group_size]. */
+int launch_quantize_nvfp4_out(const void* weight, int rows, int cols, int group_size, void* packed_out, void* scales_out,
+                              qwen35_stream_t stream);
+
+/* Replaces launch_quantize_nvfp4_lm_out (torch_bindings.cpp:83-85; kernel_gb10_nvfp4.cu:1366-1430, 1878-1892):
+ * the tensor-core layout: 16-element blocks, UE4M3 block scales in 128x4 swizzled tiles
+ * (byte = tile*512 + (row%32)*16 + ((row%128)/32)*4 + block%4, tile = (row/128)*(cols/64) + block/4), per-tensor
+ * scale 1.0.  rows must be a multiple of 128 and cols a multiple of 64. */
+int launch_quantize_nvfp4_lm_out(const void* weight, int rows, int cols, void* packed_out, void* scales_out, qwen35_stream_t stream);
+
 /* BF16 GEMM on tcgen05/TMEM tensor cores: C[M,N] = epi(A[M,K] . B[b_rows,K]^T), f32 accumulate, one
  * rounding to bf16.  Replaces cublas_bf16_gemm (prefill.cu:895-903).  lda/ldc/ldr are row strides in
  * elements; K must be a multiple of 64.  epilogue: 0 = store, 1 = + R (residual, bf16 add),

@@ -55,6 +55,8 @@ SIGNATURES = {
     "qwen35_b200_decode_steps_static": (_i, [C.POINTER(DecodeArgs), _vp]),
     "qwen35_b200_prefill_bf16": (_i, [C.POINTER(PrefillArgs), _vp]),
     "launch_prefill_bf16": (_i, [_vp, _i, _vp] + [_vp] * 5 + [_vp] * 4 + [_vp] * 3 + [_vp] * 5 + [_vp] * 5 + [_vp] * 4 + [_vp]),
+    "launch_quantize_nvfp4_out": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp]),
+    "launch_quantize_nvfp4_lm_out": (_i, [_vp, _i, _i, _vp, _vp, _vp]),
     "qwen35_b200_gemm_bf16": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "qwen35_b200_status": (_i, [_vp]),
     "qwen35_b200_clear_status": (_i, [_vp]),

@@ -55,6 +55,71 @@ def load_weights(model_name="random:1234", verbose=True, backend="bf16", device=
     return weights_to(w, device), None
 
 
+NVFP4_GROUP_SIZE = 32
+NVFP4_LM_GROUP_SIZE = 16
+NVFP4_TC_ROWS_PER_TILE = 128
+NVFP4_TC_K_PER_TILE = 64
+
+
+def _check_bf16_matrix(weight):
+    if weight.dtype != torch.bfloat16:
+        raise TypeError(f"expected bfloat16 weight, got {weight.dtype}")
+    if weight.dim() != 2:
+        raise ValueError(f"expected 2D weight, got shape {tuple(weight.shape)}")
+
+
+def _quantize_matrix_nvfp4(weight, group_size=NVFP4_GROUP_SIZE):
+    """Decode-body NVFP4 layout (reference model.py:100-114): {"packed": u8 [rows, cols/2], "scales": f16 [rows, cols/group]}."""
+    _check_bf16_matrix(weight)
+    rows, cols = weight.shape
+    if cols % 2 != 0 or cols % group_size != 0:
+        raise ValueError(f"in_dim {cols} must be divisible by 2 and group_size {group_size}")
+    w = weight.contiguous()
+    packed = torch.empty((rows, cols // 2), dtype=torch.uint8, device=w.device)
+    scales = torch.empty((rows, cols // group_size), dtype=torch.float16, device=w.device)
+    with torch.cuda.device(w.device):
+        _capi.check(_capi.lib().launch_quantize_nvfp4_out(w.data_ptr(), rows, cols, group_size, packed.data_ptr(), scales.data_ptr(),
+                                                          C.c_void_p(torch.cuda.current_stream(w.device).cuda_stream)), "quantize_nvfp4_out")
+    return {"packed": packed, "scales": scales}
+
+
+def _quantize_matrix_nvfp4_lm(weight):
+    """Tensor-core NVFP4 layout (reference model.py:117-134): 16-element blocks, swizzled E4M3 scales."""
+    _check_bf16_matrix(weight)
+    rows, cols = weight.shape
+    if rows % 128 != 0:
+        raise ValueError(f"lm_head out_dim {rows} must be divisible by 128")
+    if cols % 64 != 0:
+        raise ValueError(f"lm_head in_dim {cols} must be divisible by 64")
+    w = weight.contiguous()
+    packed = torch.empty((rows, cols // 2), dtype=torch.uint8, device=w.device)
+    scales = torch.zeros((rows // 128) * (cols // 64) * 512, dtype=torch.uint8, device=w.device)
+    with torch.cuda.device(w.device):
+        _capi.check(_capi.lib().launch_quantize_nvfp4_lm_out(w.data_ptr(), rows, cols, packed.data_ptr(), scales.data_ptr(),
+                                                             C.c_void_p(torch.cuda.current_stream(w.device).cuda_stream)), "quantize_nvfp4_lm_out")
+    return {"packed": packed, "scales": scales}
+
+
+def _quantize_matrix_nvfp4_tc(weight, padded_rows=None):
+    """The same layout for a matrix whose row count is padded with zero rows to a multiple of 128
+    (reference model.py:137-168)."""
+    _check_bf16_matrix(weight)
+    rows, cols = weight.shape
+    if cols % NVFP4_TC_K_PER_TILE != 0:
+        raise ValueError(f"in_dim {cols} must be divisible by {NVFP4_TC_K_PER_TILE}")
+    if padded_rows is None:
+        padded_rows = ((rows + NVFP4_TC_ROWS_PER_TILE - 1) // NVFP4_TC_ROWS_PER_TILE) * NVFP4_TC_ROWS_PER_TILE
+    if padded_rows < rows or padded_rows % NVFP4_TC_ROWS_PER_TILE != 0:
+        raise ValueError(f"padded_rows {padded_rows} must be a multiple of 128 and >= rows {rows}")
+    src = weight
+    if padded_rows != rows:
+        src = torch.zeros((padded_rows, cols), dtype=weight.dtype, device=weight.device)
+        src[:rows].copy_(weight)
+    out = _quantize_matrix_nvfp4_lm(src)
+    out.update(rows=rows, padded_rows=padded_rows)
+    return out
+
+
 DN_PROJ_FUSED_SIZE = DN_CONV_CHANNELS + DN_V_SIZE + 2 * DN_NUM_HEADS
 DN_PROJ_FUSED_PADDED_SIZE = ((DN_PROJ_FUSED_SIZE + 127) // 128) * 128
 PREFILL_PROJ_FUSED_SIZE = max(DN_PROJ_FUSED_PADDED_SIZE, FA_QPROJ_SIZE + 2 * FA_KV_SIZE, INTERMEDIATE_SIZE * 2)
