@@ -64,7 +64,7 @@ int launch_decode(
  * steps in one launch, feeding each arg-max back on the device. */
 typedef struct {
     const void* embed_weight;
-    const LayerWeights* layer_weights;
+    const void* layer_weights; /* LayerWeights records, or LayerWeightsNVFP4 records for the NVFP4 entry point */
     const void* final_norm_weight;
     const void* lm_head_weight;
     void* fa_k_cache;          /* bf16 [6][2][max_seq_len][256] */
@@ -133,6 +133,36 @@ typedef struct {
     int dbg_num_layers;  /* 0 = all */
 } Qwen35PrefillArgs;
 int qwen35_b200_prefill_bf16(const Qwen35PrefillArgs* args, qwen35_stream_t stream);
+
+/* NVFP4 decode.  Replaces launch_decode_nvfp4 (torch_bindings.cpp:62-77; kernel_gb10_nvfp4.cu:1999-2183) and
+ * launch_decode_many_nvfp4 (torch_bindings.cpp:87-102; kernel_gb10_nvfp4.cu:2185-2250).  layer_weights is the device
+ * table of LayerWeightsNVFP4 records {int type; int group_size; int pad[2]; void* ptrs[24]} (slot order of
+ * model.py:248-284: packed nibbles + fp16 group scales per quantised matrix, group_size 32); the LM head is in
+ * the tensor-core layout (packed + swizzled E4M3 block scales).  Weights are dequantised in registers and
+ * multiplied with the bf16 activations in f32; the reference's FP4 quantisation of the LM-head activation is
+ * not reproduced.  The input token is read from device memory so steps chain without a host round trip;
+ * launch_decode_many_nvfp4 runs `steps` steps in one launch, token_buffer[0] in/out.  The lm_hidden_* /
+ * lm_logits_f16 and scratch arguments of the reference are accepted and ignored. */
+int launch_decode_nvfp4(
+    const int* input_token_ptr, int* output_token_id, const void* embed_weight, const void* layer_weights,
+    const void* final_norm_weight, const void* lm_head_weight_packed, const void* lm_head_scales,
+    void* lm_hidden_bf16, void* lm_hidden_packed, void* lm_hidden_scales, void* lm_logits_f16,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs, void* hidden_buffer,
+    void* g_activations, void* g_residual, void* g_qkv_scratch, void* g_kv_scratch, void* g_attn_out,
+    void* g_mlp_inter, void* g_z_scratch, void* g_beta_scratch, void* g_alpha_scratch, void* g_normalized,
+    unsigned int* barrier_counter, unsigned int* barrier_generation, float* block_max_vals, int* block_max_idxs,
+    unsigned int* lm_sync_counter, int position, int max_seq_len, int group_size, qwen35_stream_t stream);
+int launch_decode_many_nvfp4(
+    int* token_buffer, int* output_tokens, int steps, const void* embed_weight, const void* layer_weights,
+    const void* final_norm_weight, const void* lm_head_weight_packed, const void* lm_head_scales,
+    void* lm_hidden_bf16, void* lm_hidden_packed, void* lm_hidden_scales, void* lm_logits_f16,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs, void* hidden_buffer,
+    void* g_activations, void* g_residual, void* g_qkv_scratch, void* g_kv_scratch, void* g_attn_out,
+    void* g_mlp_inter, void* g_z_scratch, void* g_beta_scratch, void* g_alpha_scratch, void* g_normalized,
+    unsigned int* barrier_counter, unsigned int* barrier_generation, float* block_max_vals, int* block_max_idxs,
+    unsigned int* lm_sync_counter, int position, int max_seq_len, int group_size, qwen35_stream_t stream);
+/* qwen35_b200_decode_steps for the NVFP4 format (logits, teacher forcing, debug outputs). */
+int qwen35_b200_decode_steps_nvfp4(const Qwen35DecodeArgs* args, const void* lm_head_scales, qwen35_stream_t stream);
 
 /* Replaces launch_quantize_nvfp4_out (torch_bindings.cpp:79-81; kernel_gb10_nvfp4.cu:1757-1876): pack a bf16
  * matrix [rows, cols] into the decode-body NVFP4 layout: packed uint8 [rows, cols/2] (low nibble = even

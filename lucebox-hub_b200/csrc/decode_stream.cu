@@ -26,12 +26,57 @@ namespace q35 {
 // filled by the host from a double-precision pow so that it equals torch's f32 table bit for bit.
 __constant__ float c_rope_inv_freq[FA_ROT / 2];
 
+// Layer pointers in one order for both weight formats.  *S slots are the block scales of the NVFP4 format
+// (null for bf16).  A0..A3 are the stage-A matrices: DeltaNet qkv, z, b, a; attention q, k, v.
+enum WSlot { W_IN_NORM = 0, W_POST_NORM, W_A0, W_A0S, W_A1, W_A1S, W_A2, W_A2S, W_A3, W_CONV, W_ALOG, W_DTBIAS, W_GNORM,
+             W_QNORM, W_KNORM, W_OUT, W_OUTS, W_GATE, W_GATES, W_UP, W_UPS, W_DOWN, W_DOWNS, W_NSLOTS };
+struct LayerW {
+    int type;
+    int pad;
+    const void* p[W_NSLOTS];
+};
+
+// bf16 table: struct LayerWeights (kernel.cu:77-115); NVFP4 table: struct LayerWeightsNVFP4
+// {int type; int group_size; int pad[2]; void* ptrs[24]} with the slot order of model.py:248-284.
+template <bool FP4>
+__device__ __forceinline__ void load_layer(const void* table, int layer, LayerW& out) {
+    constexpr int REC = FP4 ? 208 : 128;
+    const char* rec = (const char*)table + (size_t)layer * REC;
+    const int type = *reinterpret_cast<const int*>(rec);
+    const void* const* r = reinterpret_cast<const void* const*>(rec + 16);
+    out.type = type;
+    for (int i = 0; i < W_NSLOTS; ++i) out.p[i] = nullptr;
+    if (!FP4) {
+        if (type == 0) {
+            out.p[W_IN_NORM] = r[0]; out.p[W_A0] = r[1]; out.p[W_A1] = r[2]; out.p[W_A2] = r[3]; out.p[W_A3] = r[4];
+            out.p[W_CONV] = r[5]; out.p[W_ALOG] = r[6]; out.p[W_DTBIAS] = r[7]; out.p[W_GNORM] = r[8]; out.p[W_OUT] = r[9];
+            out.p[W_POST_NORM] = r[10]; out.p[W_GATE] = r[11]; out.p[W_UP] = r[12]; out.p[W_DOWN] = r[13];
+        } else {
+            out.p[W_IN_NORM] = r[0]; out.p[W_A0] = r[1]; out.p[W_A1] = r[2]; out.p[W_A2] = r[3]; out.p[W_QNORM] = r[4];
+            out.p[W_KNORM] = r[5]; out.p[W_OUT] = r[6]; out.p[W_POST_NORM] = r[7]; out.p[W_GATE] = r[8]; out.p[W_UP] = r[9];
+            out.p[W_DOWN] = r[10];
+        }
+    } else {
+        if (type == 0) {
+            out.p[W_IN_NORM] = r[0]; out.p[W_A0] = r[1]; out.p[W_A0S] = r[2]; out.p[W_A1] = r[3]; out.p[W_A1S] = r[4];
+            out.p[W_A2] = r[5]; out.p[W_A3] = r[6]; out.p[W_CONV] = r[7]; out.p[W_ALOG] = r[8]; out.p[W_DTBIAS] = r[9];
+            out.p[W_GNORM] = r[10]; out.p[W_OUT] = r[11]; out.p[W_OUTS] = r[12]; out.p[W_POST_NORM] = r[13];
+            out.p[W_GATE] = r[14]; out.p[W_GATES] = r[15]; out.p[W_UP] = r[16]; out.p[W_UPS] = r[17]; out.p[W_DOWN] = r[18]; out.p[W_DOWNS] = r[19];
+        } else {
+            out.p[W_IN_NORM] = r[0]; out.p[W_A0] = r[1]; out.p[W_A0S] = r[2]; out.p[W_A1] = r[3]; out.p[W_A1S] = r[4];
+            out.p[W_A2] = r[5]; out.p[W_A2S] = r[6]; out.p[W_QNORM] = r[7]; out.p[W_KNORM] = r[8]; out.p[W_OUT] = r[9]; out.p[W_OUTS] = r[10];
+            out.p[W_POST_NORM] = r[11]; out.p[W_GATE] = r[12]; out.p[W_GATES] = r[13]; out.p[W_UP] = r[14]; out.p[W_UPS] = r[15];
+            out.p[W_DOWN] = r[16]; out.p[W_DOWNS] = r[17];
+        }
+    }
+}
+
 struct Smem {
     // ring first: 16-byte aligned slots
     unsigned char ring[NSLOTS * SLOT_BYTES];
     unsigned long long full[NSLOTS];
     unsigned long long empty[NSLOTS];
-    LayerRec layers[NUM_LAYERS];
+    LayerW layers[NUM_LAYERS];
     __align__(16) bf16 x[INTER];                 // GEMV input of the current stage
     __align__(16) bf16 h[HIDDEN];                // raw layer input (residual of stage C)
     __align__(16) bf16 h1[HIDDEN];               // raw mixer output (residual of stage E)
@@ -69,63 +114,75 @@ __device__ __forceinline__ unsigned epoch_of(const DecodeArgs& a, int step, int 
 // ------------------------------------------------------------------------------------------------
 // producer: issue every weight tile of this CTA in consumption order
 // ------------------------------------------------------------------------------------------------
+// NVFP4 tile geometry (decode-body layout, group 32: 0.5 byte per weight + one fp16 scale per 32 weights).
+// Packed nibbles sit at the start of the slot, the fp16 scales of the same rows at FP4_SCALE_OFF.
+constexpr uint32_t FP4_SCALE_OFF = 8192;
+constexpr int FP4_LM_BLOCKS = VOCAB / 128;          // LM head (tensor-core layout): 1940 blocks of 128 rows
+
+template <bool FP4>
 __device__ __forceinline__ void produce(const DecodeArgs& a, Smem& s, Ring ring, const Abort& ab) {
     const int b = blockIdx.x, G = gridDim.x;
     const u64 pol = l2_policy_evict_first();
     long long next_t = clock64();
     const long long period = a.tma_period;
-    auto issue = [&](const void* src, uint32_t bytes) {
+    // one tile = one slot: `bytes` from src at the slot start and, for NVFP4, `sbytes` of scales at FP4_SCALE_OFF
+    auto issue = [&](const void* src, uint32_t bytes, const void* ssrc, uint32_t sbytes) {
         if (ab.on()) return;                       // after an abort nothing new is put in flight
         const unsigned t = ring.t;
         mbar_wait(ring.empty_bar(t), ring.phase(t) ^ 1u, ab);
         if (ab.on()) return;
-        // Pace the stream: a freed ring would otherwise be refilled in one burst by all 148 CTAs at
-        // once, and the latency-critical flagged-word traffic of the next stage queues behind it.
         long long now = clock64();
         while (now < next_t) now = clock64();
         next_t = now + period;
         ring.t = t + 1;
-        mbar_arrive_expect_tx(ring.full_bar(t), bytes);
+        mbar_arrive_expect_tx(ring.full_bar(t), bytes + sbytes);
         tma_load_1d(ring.slot_addr(t), src, bytes, ring.full_bar(t), pol);
+        if (sbytes) tma_load_1d(ring.slot_addr(t) + FP4_SCALE_OFF, ssrc, sbytes, ring.full_bar(t), pol);
+    };
+    // rows [row, row + nrows) of a [*, K] matrix
+    auto issue_rows = [&](const void* w, const void* sc, int row, int nrows, int K) {
+        if (FP4 && sc) issue((const char*)w + (size_t)row * (K / 2), (uint32_t)(nrows * (K / 2)), (const char*)sc + (size_t)row * (K / 16), (uint32_t)(nrows * (K / 16)));
+        else issue((const char*)w + (size_t)row * K * 2, (uint32_t)(nrows * K * 2), nullptr, 0);
     };
     const int n_layers = a.dbg_num_layers > 0 ? a.dbg_num_layers : NUM_LAYERS;
     for (int step = 0; step < a.n_steps; ++step) {
         for (int layer = 0; layer < n_layers; ++layer) {
-            const LayerRec& L = s.layers[layer];
-            const char *w_out, *w_gate, *w_up, *w_down;
+            const LayerW& L = s.layers[layer];
             if (L.type == 0) {
-                const char* wqkv = (const char*)L.p[DN_QKV]; const char* wz = (const char*)L.p[DN_Z];
-                const char* wb = (const char*)L.p[DN_B];     const char* wa = (const char*)L.p[DN_A];
                 for (int u = part_begin(TILES_A_DN, b, G); u < part_begin(TILES_A_DN, b + 1, G); ++u) {
                     const int v = u * 8;
-                    const char* src = v < DN_CONV_CH ? wqkv + (size_t)v * 2048
-                                    : v < DN_CONV_CH + DN_V_SIZE ? wz + (size_t)(v - DN_CONV_CH) * 2048
-                                    : v < DN_CONV_CH + DN_V_SIZE + DN_HEADS ? wb + (size_t)(v - DN_CONV_CH - DN_V_SIZE) * 2048
-                                    : wa + (size_t)(v - DN_CONV_CH - DN_V_SIZE - DN_HEADS) * 2048;
-                    issue(src, SLOT_BYTES);
+                    if (v < DN_CONV_CH) issue_rows(L.p[W_A0], L.p[W_A0S], v, 8, HIDDEN);
+                    else if (v < DN_CONV_CH + DN_V_SIZE) issue_rows(L.p[W_A1], L.p[W_A1S], v - DN_CONV_CH, 8, HIDDEN);
+                    else if (v < DN_CONV_CH + DN_V_SIZE + DN_HEADS) issue_rows(L.p[W_A2], nullptr, v - DN_CONV_CH - DN_V_SIZE, 8, HIDDEN);
+                    else issue_rows(L.p[W_A3], nullptr, v - DN_CONV_CH - DN_V_SIZE - DN_HEADS, 8, HIDDEN);
                 }
-                w_out = (const char*)L.p[DN_OUT]; w_gate = (const char*)L.p[DN_GATE]; w_up = (const char*)L.p[DN_UP]; w_down = (const char*)L.p[DN_DOWN];
             } else {
-                const char* wq = (const char*)L.p[FA_Q]; const char* wk = (const char*)L.p[FA_K]; const char* wv = (const char*)L.p[FA_V];
                 for (int u = part_begin(TILES_A_FA, b, G); u < part_begin(TILES_A_FA, b + 1, G); ++u) {
                     const int v = u * 8;
-                    const char* src = v < FA_QPROJ ? wq + (size_t)v * 2048
-                                    : v < FA_QPROJ + FA_KV_SIZE ? wk + (size_t)(v - FA_QPROJ) * 2048
-                                    : wv + (size_t)(v - FA_QPROJ - FA_KV_SIZE) * 2048;
-                    issue(src, SLOT_BYTES);
+                    if (v < FA_QPROJ) issue_rows(L.p[W_A0], L.p[W_A0S], v, 8, HIDDEN);
+                    else if (v < FA_QPROJ + FA_KV_SIZE) issue_rows(L.p[W_A1], L.p[W_A1S], v - FA_QPROJ, 8, HIDDEN);
+                    else issue_rows(L.p[W_A2], L.p[W_A2S], v - FA_QPROJ - FA_KV_SIZE, 8, HIDDEN);
                 }
-                w_out = (const char*)L.p[FA_O]; w_gate = (const char*)L.p[FA_GATE]; w_up = (const char*)L.p[FA_UP]; w_down = (const char*)L.p[FA_DOWN];
             }
-            for (int u = part_begin(TILES_C, b, G); u < part_begin(TILES_C, b + 1, G); ++u) issue(w_out + (size_t)u * SLOT_BYTES, SLOT_BYTES);
+            for (int u = part_begin(TILES_C, b, G); u < part_begin(TILES_C, b + 1, G); ++u) issue_rows(L.p[W_OUT], L.p[W_OUTS], u * 4, 4, 2048);
             for (int u = part_begin(UNITS_D, b, G); u < part_begin(UNITS_D, b + 1, G); ++u) {
-                issue(w_gate + (size_t)u * SLOT_BYTES, SLOT_BYTES);
-                issue(w_up + (size_t)u * SLOT_BYTES, SLOT_BYTES);
+                issue_rows(L.p[W_GATE], L.p[W_GATES], u * 8, 8, HIDDEN);
+                issue_rows(L.p[W_UP], L.p[W_UPS], u * 8, 8, HIDDEN);
             }
-            for (int u = part_begin(TILES_E, b, G); u < part_begin(TILES_E, b + 1, G); ++u) issue(w_down + (size_t)u * 14336, 14336);
+            for (int u = part_begin(TILES_E, b, G); u < part_begin(TILES_E, b + 1, G); ++u) issue_rows(L.p[W_DOWN], L.p[W_DOWNS], u * 2, 2, INTER);
         }
-        if (!a.lm_last_only || step == a.n_steps - 1)
-            for (int u = part_begin(TILES_LM, b, G); u < part_begin(TILES_LM, b + 1, G); ++u)
-                issue((const char*)a.lm_head + (size_t)u * SLOT_BYTES, SLOT_BYTES);
+        if (!a.lm_last_only || step == a.n_steps - 1) {
+            if (!FP4) {
+                for (int u = part_begin(TILES_LM, b, G); u < part_begin(TILES_LM, b + 1, G); ++u)
+                    issue((const char*)a.lm_head + (size_t)u * SLOT_BYTES, SLOT_BYTES, nullptr, 0);
+            } else {
+                // per 128-row block: its 8 KB of swizzled E4M3 scales, then four 32-row tiles of packed nibbles
+                for (int blk = part_begin(FP4_LM_BLOCKS, b, G); blk < part_begin(FP4_LM_BLOCKS, b + 1, G); ++blk) {
+                    issue((const char*)a.lm_scales + (size_t)blk * 8192, 8192, nullptr, 0);
+                    for (int q = 0; q < 4; ++q) issue((const char*)a.lm_head + ((size_t)blk * 128 + q * 32) * 512, 16384, nullptr, 0);
+                }
+            }
+        }
     }
     // drain: every copy this CTA issued must have landed before the CTA may exit
     const unsigned issued = ring.t;
@@ -175,6 +232,87 @@ __device__ __forceinline__ void consume_k1024(Ring& ring, int n_units, const bf1
     ring.t = t0 + (unsigned)(n_units * NMAT);
 }
 
+// ---- NVFP4 (E2M1 + block scale) dequantisation in registers ----
+__device__ __forceinline__ float2 fp4x2_to_float2(uint32_t byte) {
+    const __half2_raw h = __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)byte, __NV_E2M1);   // low nibble -> .x
+    return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+// 32 E2M1 weights (16 bytes) times 32 activations, f32 accumulate; the block scale is applied by the caller
+__device__ __forceinline__ float dot32_fp4(const uint4 p, const float* x) {
+    const uint32_t w[4] = {p.x, p.y, p.z, p.w};
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int bb = 0; bb < 4; ++bb) {
+            const float2 f = fp4x2_to_float2((w[i] >> (8 * bb)) & 0xffu);
+            a0 = fmaf(f.x, x[i * 8 + bb * 2], a0);
+            a1 = fmaf(f.y, x[i * 8 + bb * 2 + 1], a1);
+        }
+    return a0 + a1;
+}
+// the two halves (16 weights each) separately: tensor-core layout has one scale per 16 weights
+__device__ __forceinline__ float2 dot16x2_fp4(const uint4 p, const float* x) {
+    const uint32_t w[4] = {p.x, p.y, p.z, p.w};
+    float a[2] = {0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int bb = 0; bb < 4; ++bb) {
+            const float2 f = fp4x2_to_float2((w[i] >> (8 * bb)) & 0xffu);
+            a[i >> 1] = fmaf(f.x, x[i * 8 + bb * 2], a[i >> 1]);
+            a[i >> 1] = fmaf(f.y, x[i * 8 + bb * 2 + 1], a[i >> 1]);
+        }
+    return make_float2(a[0], a[1]);
+}
+__device__ __forceinline__ float lds_half(uint32_t addr) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+    return __half2float(__ushort_as_half(v));
+}
+__device__ __forceinline__ float2 lds_e4m3x2(uint32_t addr) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)v, __NV_E4M3);
+    return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+// 32 consecutive activations starting at element e0 (a multiple of 32)
+__device__ __forceinline__ void load_x32(const bf16* xs, int e0, float* x) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) unpack8(*reinterpret_cast<const uint4*>(xs + e0 + 8 * j), x + 8 * j);
+}
+
+// NVFP4 version of consume_k1024: a row is 512 bytes of nibbles, lane l owns elements [32 l, 32 l + 32), which
+// is exactly one scale group, so the scale is applied once per (row, lane) after the dot product.
+template <int NMAT, typename Epi>
+__device__ __forceinline__ void consume_k1024_fp4(Ring& ring, int n_units, const bf16* xs, const Abort& ab, Epi epi) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float x[32];
+    load_x32(xs, 32 * lane, x);
+    const unsigned t0 = ring.t;
+    for (int g = 0; g < n_units; g += 4) {
+        const int ui = g + (warp >> 2);
+        if (ui < n_units) {
+            float acc[NMAT][2];
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) {
+                const unsigned tile = t0 + (unsigned)(ui * NMAT + m);
+                mbar_wait(ring.full_bar(tile), ring.phase(tile), ab);
+                const uint32_t r0 = (uint32_t)(2 * (warp & 3));
+                const uint32_t base = ring.slot_addr(tile) + r0 * 512u + (uint32_t)lane * 16u;
+                const uint32_t sbase = ring.slot_addr(tile) + FP4_SCALE_OFF + r0 * 64u + (uint32_t)lane * 2u;
+                const uint4 p0 = lds128(base), p1 = lds128(base + 512);
+                const float s0 = lds_half(sbase), s1 = lds_half(sbase + 64);
+                acc[m][0] = warp_sum(dot32_fp4(p0, x) * s0);
+                acc[m][1] = warp_sum(dot32_fp4(p1, x) * s1);
+                if (lane == 0) mbar_arrive(ring.empty_bar(tile), 4);
+            }
+            if (lane == 0) epi(ui * 8 + 2 * (warp & 3), acc);
+        }
+    }
+    ring.t = t0 + (unsigned)(n_units * NMAT);
+}
+
 __device__ __forceinline__ void poll2(const u64* p0, const u64* p1, uint32_t epoch, const Abort& ab, uint32_t& o0, uint32_t& o1) {
     uint32_t o[2];
     poll_n<2>(p0, (int)(p1 - p0), 2, epoch, ab, o);
@@ -197,6 +335,7 @@ __device__ __forceinline__ void rmsnorm_pair(uint32_t raw, const bf16* w, bf16* 
 // ------------------------------------------------------------------------------------------------
 // kernel
 // ------------------------------------------------------------------------------------------------
+template <bool FP4>
 __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const DecodeArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     Smem& s = *reinterpret_cast<Smem*>(smem_raw);
@@ -214,15 +353,14 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
         }
         mbar_fence_init();
     }
-    for (int i = tid; i < NUM_LAYERS * (int)(sizeof(LayerRec) / 16); i += STREAM_THREADS)
-        reinterpret_cast<uint4*>(s.layers)[i] = __ldg(reinterpret_cast<const uint4*>(a.layers) + i);
+    if (tid < NUM_LAYERS) load_layer<FP4>(a.layers, tid, s.layers[tid]);
     __syncthreads();
 
     Abort ab{&s.abort_flag, &ws->err};
     Ring ring{smem_u32(s.ring), smem_u32(s.full), smem_u32(s.empty), 0u};
 
     if (warp == NCONS_WARPS) {
-        if (lane == 0) produce(a, s, ring, ab);
+        if (lane == 0) produce<FP4>(a, s, ring, ab);
         __syncwarp();
     } else {
         // =========================== consumers ===========================
@@ -236,12 +374,12 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
             int i_dn = 0, i_fa = 0;
 
             for (int layer = 0; layer < n_layers; ++layer) {
-                const LayerRec& L = s.layers[layer];
+                const LayerW& L = s.layers[layer];
                 const int stamp_row = layer;
                 Q35_STAMP(0);
                 const unsigned ep = epoch_of(a, step, layer);
                 const bool dn = (L.type == 0);
-                const bf16* w_post = (const bf16*)(dn ? L.p[DN_POST_NORM] : L.p[FA_POST_NORM]);
+                const bf16* w_post = (const bf16*)L.p[W_POST_NORM];
 
                 // ---- DeltaNet: issue the state / conv loads of stage B before any waiting ----
                 const int pp0 = part_begin(DN_V_SIZE / 2, b, G), pp1 = part_begin(DN_V_SIZE / 2, b + 1, G);   // value-row pairs
@@ -264,14 +402,26 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                     else if (a.dbg_teacher) raw = __ldg(reinterpret_cast<const uint32_t*>(a.dbg_teacher + layer * HIDDEN) + tid);
                     else raw = poll_word(&ws->h2[tid], epoch_of(a, step, layer - 1), ab);
                     reinterpret_cast<uint32_t*>(s.h)[tid] = raw;
-                    rmsnorm_pair(raw, (const bf16*)L.p[0], s.x, s.red);
+                    rmsnorm_pair(raw, (const bf16*)L.p[W_IN_NORM], s.x, s.red);
                     cons_sync();
                     Q35_STAMP(1);
                     const int ntl = dn ? TILES_A_DN : TILES_A_FA;
                     const int u0 = part_begin(ntl, b, G), u1 = part_begin(ntl, b + 1, G);
-                    consume_k1024<1>(ring, u1 - u0, s.x, ab, [&](int row, const float (*acc)[2]) {
-                        s.stage[row >> 1] = pack_bf16x2(acc[0][0], acc[0][1]);
-                    });
+                    if (FP4) {
+                        // qkv / z (or q, k, v) tiles are NVFP4; the 16+16 rows of the b and a projections stay bf16
+                        const int n_q = dn ? max(0, min(u1, (DN_CONV_CH + DN_V_SIZE) / 8) - u0) : (u1 - u0);
+                        consume_k1024_fp4<1>(ring, n_q, s.x, ab, [&](int row, const float (*acc)[2]) {
+                            s.stage[row >> 1] = pack_bf16x2(acc[0][0], acc[0][1]);
+                        });
+                        if (u1 - u0 > n_q)
+                            consume_k1024<1>(ring, u1 - u0 - n_q, s.x, ab, [&](int row, const float (*acc)[2]) {
+                                s.stage[(n_q * 8 + row) >> 1] = pack_bf16x2(acc[0][0], acc[0][1]);
+                            });
+                    } else {
+                        consume_k1024<1>(ring, u1 - u0, s.x, ab, [&](int row, const float (*acc)[2]) {
+                            s.stage[row >> 1] = pack_bf16x2(acc[0][0], acc[0][1]);
+                        });
+                    }
                     // one coalesced store per CTA: a line that is written once reaches its pollers fastest
                     cons_sync();
                     if (tid < (u1 - u0) * 4) st_word(&ws->xa[u0 * 4 + tid], s.stage[tid], ep);
@@ -280,7 +430,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                 Q35_STAMP_ALL(2);
                 if (dn) {
                     // ================= stage B (DeltaNet): conv, norms, recurrence =================
-                    const bf16* conv_w = (const bf16*)L.p[DN_CONV];
+                    const bf16* conv_w = (const bf16*)L.p[W_CONV];
                     const int hlo = (2 * pp0) >> 7, hhi = (pp1 > pp0) ? ((2 * pp1 - 1) >> 7) : hlo;   // at most two heads per CTA
                     uint32_t vw_pre = 0;
                     {
@@ -320,9 +470,9 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                             const uint32_t aw = poll_word(&ws->xa[(DN_CONV_CH + DN_V_SIZE + DN_HEADS + h) >> 1], ep, ab);
                             const float bb = (h & 1) ? bf_hi(bw) : bf_lo(bw);
                             const float aa = (h & 1) ? bf_hi(aw) : bf_lo(aw);
-                            const float x = aa + bf2f(((const bf16*)L.p[DN_DTBIAS])[h]);
+                            const float x = aa + bf2f(((const bf16*)L.p[W_DTBIAS])[h]);
                             const float sp = (x > 20.f) ? x : log1pf(expf(x));
-                            const float g = -expf(bf2f(((const bf16*)L.p[DN_ALOG])[h])) * sp;
+                            const float g = -expf(bf2f(((const bf16*)L.p[W_ALOG])[h])) * sp;
                             s.hd[sl][0] = rbf(sigmoid_f(bb));
                             s.hd[sl][1] = expf(g);
                         }
@@ -370,7 +520,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                             z0 = ((uint32_t)(b0 >> 32) == ep) ? (uint32_t)b0 : poll_word(pz, ep, ab);
                             z1 = ((uint32_t)(b1 >> 32) == ep) ? (uint32_t)b1 : poll_word(pz + 1, ep, ab);
                         }
-                        const uint2 nrw = __ldg(reinterpret_cast<const uint2*>(L.p[DN_NORM]) + lane);
+                        const uint2 nrw = __ldg(reinterpret_cast<const uint2*>(L.p[W_GNORM]) + lane);
                         const float ov[4] = {bf_lo(o0), bf_hi(o0), bf_lo(o1), bf_hi(o1)};
                         const float zv[4] = {bf_lo(z0), bf_hi(z0), bf_lo(z1), bf_hi(z1)};
                         const float nw[4] = {bf_lo(nrw.x), bf_hi(nrw.x), bf_lo(nrw.y), bf_hi(nrw.y)};
@@ -402,7 +552,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                             // lane l holds elements {2l, 2l+1} + 64*i, i = 0..3 (four flagged words)
                             const bool isq = warp < FA_GQA;
                             const int e0 = isq ? (kvh * FA_GQA + warp) * 2 * FA_HEAD_DIM : FA_QPROJ + kvh * FA_HEAD_DIM;
-                            const bf16* nw = (const bf16*)(isq ? L.p[FA_QNORM] : L.p[FA_KNORM]);
+                            const bf16* nw = (const bf16*)(isq ? L.p[W_QNORM] : L.p[W_KNORM]);
                             float xv[8], ss = 0.f;
                             uint32_t wv[4];
                             poll4(&ws->xa[(e0 >> 1) + lane], 32, ep, ab, wv);
@@ -588,6 +738,26 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                 {
                     const bf16* hin = s.h;
                     const int u0 = part_begin(TILES_C, b, G), nt = part_begin(TILES_C, b + 1, G) - u0;
+                    if (FP4) {
+                        // 4 rows x 1024 bytes of nibbles per tile; warps 0-7: row w/2, K half w%2 (32 groups of 32, one per lane)
+                        float x[32];
+                        if (warp < 8) load_x32(s.x, (warp & 1) * 1024 + 32 * lane, x);
+                        for (int ti = 0; ti < nt; ++ti) {
+                            const unsigned tile = ring.t + (unsigned)ti;
+                            if (warp < 8) {
+                                mbar_wait(ring.full_bar(tile), ring.phase(tile), ab);
+                                const uint32_t row = (uint32_t)(warp >> 1), half = (uint32_t)(warp & 1);
+                                const uint4 pk = lds128(ring.slot_addr(tile) + row * 1024u + half * 512u + (uint32_t)lane * 16u);
+                                const float sc = lds_half(ring.slot_addr(tile) + FP4_SCALE_OFF + row * 128u + (half * 32u + (uint32_t)lane) * 2u);
+                                const float acc = warp_sum(dot32_fp4(pk, x) * sc);
+                                if (lane == 0) {
+                                    s.part[ti * 16 + row * 4 + half] = acc;
+                                    s.part[ti * 16 + row * 4 + 2 + half] = 0.f;
+                                    mbar_arrive(ring.empty_bar(tile), 2);
+                                }
+                            }
+                        }
+                    } else {
                     float x[16];
                     unpack8(*reinterpret_cast<const uint4*>(s.x + (warp & 3) * 512 + lane * 8), x);
                     unpack8(*reinterpret_cast<const uint4*>(s.x + (warp & 3) * 512 + (32 + lane) * 8), x + 8);
@@ -598,6 +768,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                         const uint4 q0 = lds128(base), q1 = lds128(base + 512);
                         const float acc = warp_sum(dot8(q1, x + 8, dot8(q0, x, 0.f)));
                         if (lane == 0) { s.part[ti * 16 + warp] = acc; mbar_arrive(ring.empty_bar(tile), 1); }
+                    }
                     }
                     ring.t += (unsigned)nt;
                     cons_sync();
@@ -632,11 +803,13 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                     cons_sync();
                     Q35_STAMP(6);
                     const int u0 = part_begin(UNITS_D, b, G), u1 = part_begin(UNITS_D, b + 1, G);
-                    consume_k1024<2>(ring, u1 - u0, s.x, ab, [&](int row, const float (*acc)[2]) {
+                    auto epi_d = [&](int row, const float (*acc)[2]) {
                         const float m0 = rbf(silu_f(rbf(acc[0][0]))) * rbf(acc[1][0]);
                         const float m1 = rbf(silu_f(rbf(acc[0][1]))) * rbf(acc[1][1]);
                         s.stage[row >> 1] = pack_bf16x2(m0, m1);
-                    });
+                    };
+                    if (FP4) consume_k1024_fp4<2>(ring, u1 - u0, s.x, ab, epi_d);
+                    else consume_k1024<2>(ring, u1 - u0, s.x, ab, epi_d);
                     cons_sync();
                     if (tid < (u1 - u0) * 4) st_word(&ws->m[u0 * 4 + tid], s.stage[tid], ep);
                 }
@@ -655,6 +828,30 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                     cons_sync();
                     Q35_STAMP(8);
                     const int u0 = part_begin(TILES_E, b, G), nt = part_begin(TILES_E, b + 1, G) - u0;
+                    if (FP4) {
+                        // 2 rows x 1792 bytes of nibbles per tile; warp: tile w/4, row (w%4)/2, K half w%2 = 56 groups of 32:
+                        // lane l takes group l and, for l < 24, group 32 + l
+                        const int half = warp & 1;
+                        for (int g = 0; g < nt; g += 4) {
+                            const int ti = g + (warp >> 2);
+                            if (ti < nt) {
+                                const unsigned tile = ring.t + (unsigned)ti;
+                                mbar_wait(ring.full_bar(tile), ring.phase(tile), ab);
+                                const uint32_t row = (uint32_t)((warp & 3) >> 1);
+                                const uint32_t pb = ring.slot_addr(tile) + row * 1792u + (uint32_t)half * 896u + (uint32_t)lane * 16u;
+                                const uint32_t sb = ring.slot_addr(tile) + FP4_SCALE_OFF + row * 224u + ((uint32_t)half * 56u + (uint32_t)lane) * 2u;
+                                float x[32];          // a CTA owns at most four of these tiles, so each warp runs this once per stage
+                                load_x32(s.x, half * 1792 + 32 * lane, x);
+                                float acc = dot32_fp4(lds128(pb), x) * lds_half(sb);
+                                if (lane < 24) {
+                                    load_x32(s.x, half * 1792 + 32 * (32 + lane), x);
+                                    acc += dot32_fp4(lds128(pb + 512), x) * lds_half(sb + 64);
+                                }
+                                acc = warp_sum(acc);
+                                if (lane == 0) { s.part[ti * 4 + (warp & 3)] = acc; mbar_arrive(ring.empty_bar(tile), 4); }
+                            }
+                        }
+                    } else {
                     uint4 xp[7];
 #pragma unroll
                     for (int j = 0; j < 7; ++j) xp[j] = *reinterpret_cast<const uint4*>(s.x + (warp & 1) * 1792 + (j * 32 + lane) * 8);
@@ -670,6 +867,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                             acc = warp_sum(acc);
                             if (lane == 0) { s.part[ti * 4 + (warp & 3)] = acc; mbar_arrive(ring.empty_bar(tile), 4); }
                         }
+                    }
                     }
                     ring.t += (unsigned)nt;
                     cons_sync();
@@ -697,14 +895,50 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                 float best = -INFINITY;
                 int best_i = 0x7fffffff;
                 float* lg = (last_step ? a.logits_out : nullptr);
-                const int u0 = part_begin(TILES_LM, b, G), u1 = part_begin(TILES_LM, b + 1, G);
-                consume_k1024<1>(ring, u1 - u0, s.x, ab, [&](int row, const float (*acc)[2]) {
-                    const int r0 = u0 * 8 + row;
-                    const float v0 = rbf(acc[0][0]), v1 = rbf(acc[0][1]);
-                    if (lg) { lg[r0] = v0; lg[r0 + 1] = v1; }
-                    if (v0 > best) { best = v0; best_i = r0; }
-                    if (v1 > best) { best = v1; best_i = r0 + 1; }
-                });
+                // rows of the vocabulary owned by this CTA: [lm_row0, ...), in 8-row tiles (bf16) or 128-row blocks (NVFP4)
+                const int lm_row0 = FP4 ? part_begin(FP4_LM_BLOCKS, b, G) * 128 : part_begin(TILES_LM, b, G) * 8;
+                if (FP4) {
+                    // tensor-core layout: one E4M3 scale per 16 weights, stored in 512-byte tiles of 128 rows x 4 blocks
+                    float x[32];
+                    load_x32(s.x, 32 * lane, x);
+                    const int B0 = part_begin(FP4_LM_BLOCKS, b, G), B1 = part_begin(FP4_LM_BLOCKS, b + 1, G);
+                    for (int blk = B0; blk < B1; ++blk) {
+                        const unsigned tile_s = ring.t, tile_p = ring.t + 1u + (unsigned)(warp >> 2);
+                        mbar_wait(ring.full_bar(tile_s), ring.phase(tile_s), ab);
+                        mbar_wait(ring.full_bar(tile_p), ring.phase(tile_p), ab);
+                        const uint32_t sp = ring.slot_addr(tile_p), ss = ring.slot_addr(tile_s);
+#pragma unroll
+                        for (int it = 0; it < 4; ++it) {
+                            float vv[2];
+#pragma unroll
+                            for (int r = 0; r < 2; ++r) {
+                                const uint32_t rit = (uint32_t)((warp & 3) * 8 + it * 2 + r);           // row inside the 32-row tile
+                                const uint4 pk = lds128(sp + rit * 512u + (uint32_t)lane * 16u);
+                                const float2 sc = lds_e4m3x2(ss + (uint32_t)(lane >> 1) * 512u + rit * 16u + (uint32_t)(warp >> 2) * 4u + (uint32_t)((2 * lane) & 3));
+                                const float2 d = dot16x2_fp4(pk, x);
+                                vv[r] = warp_sum(d.x * sc.x + d.y * sc.y);
+                            }
+                            if (lane == 0) {
+                                const int r0 = blk * 128 + (warp >> 2) * 32 + (warp & 3) * 8 + it * 2;
+                                const float v0 = rbf(vv[0]), v1 = rbf(vv[1]);
+                                if (lg) { lg[r0] = v0; lg[r0 + 1] = v1; }
+                                if (v0 > best) { best = v0; best_i = r0; }
+                                if (v1 > best) { best = v1; best_i = r0 + 1; }
+                            }
+                        }
+                        if (lane == 0) { mbar_arrive(ring.empty_bar(tile_p), 4); mbar_arrive(ring.empty_bar(tile_s), 1); }
+                        ring.t += 5u;
+                    }
+                } else {
+                    const int u0 = part_begin(TILES_LM, b, G), u1 = part_begin(TILES_LM, b + 1, G);
+                    consume_k1024<1>(ring, u1 - u0, s.x, ab, [&](int row, const float (*acc)[2]) {
+                        const int r0 = u0 * 8 + row;
+                        const float v0 = rbf(acc[0][0]), v1 = rbf(acc[0][1]);
+                        if (lg) { lg[r0] = v0; lg[r0 + 1] = v1; }
+                        if (v0 > best) { best = v0; best_i = r0; }
+                        if (v1 > best) { best = v1; best_i = r0 + 1; }
+                    });
+                }
                 Q35_STAMP(2);
                 // lane 0 of every warp holds that warp's best (rows ascend within a warp)
                 cons_sync();
@@ -717,7 +951,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                         if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
                     }
                     // bf16 value in the high half, row offset inside this CTA's range (< 2048) in the low half
-                    st_word(&ws->lm[0][b], (__float_as_uint(bv) & 0xffff0000u) | (uint32_t)(bi - u0 * 8), ep_lm);
+                    st_word(&ws->lm[0][b], (__float_as_uint(bv) & 0xffff0000u) | (uint32_t)(bi - lm_row0), ep_lm);
                 }
                 if (warp == 0) {
                     constexpr int PER = 8;                               // up to 256 CTAs
@@ -731,7 +965,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                         if (c < G) {
                             const uint32_t w = ((uint32_t)(v[k] >> 32) == ep_lm) ? (uint32_t)v[k] : poll_word(&ws->lm[0][c], ep_lm, ab);
                             const float val = __uint_as_float(w & 0xffff0000u);
-                            const int idx = part_begin(TILES_LM, c, G) * 8 + (int)(w & 0xffffu);
+                            const int idx = (FP4 ? part_begin(FP4_LM_BLOCKS, c, G) * 128 : part_begin(TILES_LM, c, G) * 8) + (int)(w & 0xffffu);
                             if (val > bv || (val == bv && idx < bi)) { bv = val; bi = idx; }
                         }
                     }
@@ -803,7 +1037,7 @@ static int tma_period() {
     return v;
 }
 
-static int launch_decode_impl(const DecodeArgs& in, cudaStream_t stream, bool use_static = false) {
+static int launch_decode_impl(const DecodeArgs& in, cudaStream_t stream, bool use_static = false, bool fp4 = false) {
     static std::once_flag once[64];
     static bool ready[64] = {};
     int dev = 0;
@@ -813,9 +1047,12 @@ static int launch_decode_impl(const DecodeArgs& in, cudaStream_t stream, bool us
         float t[FA_ROT / 2];
         rope_table(t);
         int nb = 0;
+        int nb2 = 0;
         if (cudaMemcpyToSymbol(c_rope_inv_freq, t, sizeof(t)) == cudaSuccess &&
-            cudaFuncSetAttribute(decode_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem)) == cudaSuccess &&
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, decode_stream_kernel, STREAM_THREADS, sizeof(Smem)) == cudaSuccess && nb >= 1)
+            cudaFuncSetAttribute(decode_stream_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem)) == cudaSuccess &&
+            cudaFuncSetAttribute(decode_stream_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(Smem)) == cudaSuccess &&
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, decode_stream_kernel<false>, STREAM_THREADS, sizeof(Smem)) == cudaSuccess && nb >= 1 &&
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb2, decode_stream_kernel<true>, STREAM_THREADS, sizeof(Smem)) == cudaSuccess && nb2 >= 1)
             ready[dev] = true;
     });
     if (!ready[dev]) { set_error("decode kernel cannot be made resident on this device (needs %zu bytes of shared memory)", sizeof(Smem)); return QWEN35_ERR_CUDA; }
@@ -865,7 +1102,9 @@ static int launch_decode_impl(const DecodeArgs& in, cudaStream_t stream, bool us
     a.tma_period = tma_period();
     *epoch += (unsigned)(32u * (unsigned)a.n_steps);
     void* params[] = {(void*)&a};
-    Q35_CUDA_OK(cudaLaunchCooperativeKernel((const void*)decode_stream_kernel, dim3(decode_grid()), dim3(STREAM_THREADS), params, sizeof(Smem), stream));
+    if (fp4 && !a.lm_scales) { set_error("NVFP4 decode needs the LM-head scales"); return QWEN35_ERR_BAD_ARG; }
+    const void* kern = fp4 ? (const void*)decode_stream_kernel<true> : (const void*)decode_stream_kernel<false>;
+    Q35_CUDA_OK(cudaLaunchCooperativeKernel(kern, dim3(decode_grid()), dim3(STREAM_THREADS), params, sizeof(Smem), stream));
     g_launches.fetch_add(1);
     return QWEN35_OK;
 }
@@ -883,7 +1122,7 @@ extern "C" int launch_decode(
     unsigned int*, unsigned int*, float*, int*, unsigned int*,
     int position, int max_seq_len, qwen35_stream_t stream) {
     q35::DecodeArgs a = {};
-    a.layers = reinterpret_cast<const q35::LayerRec*>(layer_weights);
+    a.layers = layer_weights;
     a.embed = (const q35::bf16*)embed_weight;
     a.final_norm = (const q35::bf16*)final_norm_weight;
     a.lm_head = (const q35::bf16*)lm_head_weight;
@@ -900,10 +1139,10 @@ extern "C" int launch_decode(
     return q35::launch_decode_impl(a, (cudaStream_t)stream);
 }
 
-static int decode_steps_common(const Qwen35DecodeArgs* in, qwen35_stream_t stream, bool use_static) {
+static int decode_steps_common(const Qwen35DecodeArgs* in, qwen35_stream_t stream, bool use_static, bool fp4 = false, const void* lm_scales = nullptr) {
     if (!in) { q35::set_error("null args"); return QWEN35_ERR_BAD_ARG; }
     q35::DecodeArgs a = {};
-    a.layers = reinterpret_cast<const q35::LayerRec*>(in->layer_weights);
+    a.layers = in->layer_weights;
     a.embed = (const q35::bf16*)in->embed_weight;
     a.final_norm = (const q35::bf16*)in->final_norm_weight;
     a.lm_head = (const q35::bf16*)in->lm_head_weight;
@@ -927,7 +1166,8 @@ static int decode_steps_common(const Qwen35DecodeArgs* in, qwen35_stream_t strea
     a.dbg_num_layers = in->dbg_num_layers;
     a.dbg_time = in->dbg_time;
     a.dbg_time_cta = in->dbg_time_cta;
-    return q35::launch_decode_impl(a, (cudaStream_t)stream, use_static);
+    a.lm_scales = lm_scales;
+    return q35::launch_decode_impl(a, (cudaStream_t)stream, use_static, fp4);
 }
 
 extern "C" int qwen35_b200_decode_steps(const Qwen35DecodeArgs* in, qwen35_stream_t stream) {
@@ -944,6 +1184,53 @@ extern "C" int qwen35_b200_decode_steps_static(const Qwen35DecodeArgs* in, qwen3
         return QWEN35_ERR_BAD_ARG;
     }
     return decode_steps_common(in, stream, true);
+}
+
+// ---- NVFP4 decode (reference: launch_decode_nvfp4 / launch_decode_many_nvfp4, kernel_gb10_nvfp4.cu:1999-2250) ----
+static int nvfp4_common(const int* token_in, int* out_token, int* out_tokens, int steps,
+                        const void* embed, const void* layers, const void* final_norm, const void* lm_packed, const void* lm_scales,
+                        void* k_cache, void* v_cache, void* dn_states, void* conv_bufs, void* hidden, int position, int max_seq_len,
+                        int group_size, qwen35_stream_t stream) {
+    if (group_size != 32) { q35::set_error("NVFP4 decode supports group_size 32 (got %d)", group_size); return QWEN35_ERR_UNSUPPORTED; }
+    if (!token_in) { q35::set_error("null token pointer"); return QWEN35_ERR_BAD_ARG; }
+    q35::DecodeArgs a = {};
+    a.layers = layers; a.embed = (const q35::bf16*)embed; a.final_norm = (const q35::bf16*)final_norm;
+    a.lm_head = (const q35::bf16*)lm_packed; a.lm_scales = lm_scales;
+    a.k_cache = (q35::bf16*)k_cache; a.v_cache = (q35::bf16*)v_cache; a.dn_states = (float*)dn_states; a.conv_bufs = (float*)conv_bufs;
+    a.token_in = token_in; a.out_token = out_token; a.out_tokens = out_tokens; a.hidden_out = (q35::bf16*)hidden;
+    a.position = position; a.max_seq_len = max_seq_len; a.n_steps = steps;
+    return q35::launch_decode_impl(a, (cudaStream_t)stream, false, true);
+}
+
+extern "C" int launch_decode_nvfp4(
+    const int* input_token_ptr, int* output_token_id, const void* embed_weight, const void* layer_weights,
+    const void* final_norm_weight, const void* lm_head_weight_packed, const void* lm_head_scales,
+    void*, void*, void*, void*,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs, void* hidden_buffer,
+    void*, void*, void*, void*, void*, void*, void*, void*, void*, void*,
+    unsigned int*, unsigned int*, float*, int*, unsigned int*,
+    int position, int max_seq_len, int group_size, qwen35_stream_t stream) {
+    return nvfp4_common(input_token_ptr, output_token_id, nullptr, 1, embed_weight, layer_weights, final_norm_weight, lm_head_weight_packed,
+                        lm_head_scales, fa_k_cache, fa_v_cache, dn_states, conv_bufs, hidden_buffer, position, max_seq_len, group_size, stream);
+}
+
+extern "C" int launch_decode_many_nvfp4(
+    int* token_buffer, int* output_tokens, int steps, const void* embed_weight, const void* layer_weights,
+    const void* final_norm_weight, const void* lm_head_weight_packed, const void* lm_head_scales,
+    void*, void*, void*, void*,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs, void* hidden_buffer,
+    void*, void*, void*, void*, void*, void*, void*, void*, void*, void*,
+    unsigned int*, unsigned int*, float*, int*, unsigned int*,
+    int position, int max_seq_len, int group_size, qwen35_stream_t stream) {
+    // token_buffer[0] holds the first input token and receives the last generated one, as in the reference
+    return nvfp4_common(token_buffer, token_buffer, output_tokens, steps, embed_weight, layer_weights, final_norm_weight, lm_head_weight_packed,
+                        lm_head_scales, fa_k_cache, fa_v_cache, dn_states, conv_bufs, hidden_buffer, position, max_seq_len, group_size, stream);
+}
+
+// Extended NVFP4 decode: the arguments of qwen35_b200_decode_steps (layer table in the NVFP4 record layout,
+// lm_head_weight = packed nibbles) plus the LM-head scales.
+extern "C" int qwen35_b200_decode_steps_nvfp4(const Qwen35DecodeArgs* in, const void* lm_head_scales, qwen35_stream_t stream) {
+    return decode_steps_common(in, stream, false, true, lm_head_scales);
 }
 
 // Debug: synchronise the device and decode one flagged-word vector of the workspace to bf16 on the host.

@@ -7,6 +7,10 @@
 //     both the data and the proof that it is current -- no grid barrier, no fence on the path.
 #pragma once
 
+#include <cuda_fp16.h>
+#include <cuda_fp4.h>
+#include <cuda_fp8.h>
+
 #include "common.cuh"
 
 namespace q35 {
@@ -47,10 +51,11 @@ struct StreamWorkspace {
 };
 
 struct DecodeArgs {
-    const LayerRec* layers;
+    const void* layers;       // device table: LayerWeights (bf16) or LayerWeightsNVFP4 records
     const bf16* embed;
     const bf16* final_norm;
-    const bf16* lm_head;
+    const bf16* lm_head;      // bf16 [V,1024], or packed E2M1 [V,512] for NVFP4
+    const void* lm_scales;    // NVFP4: swizzled E4M3 block scales of the LM head (tensor-core layout)
     bf16* k_cache;
     bf16* v_cache;
     float* dn_states;

@@ -52,6 +52,9 @@ _vp, _i = C.c_void_p, C.c_int
 SIGNATURES = {
     "launch_decode": (_i, [_i, _vp] + [_vp] * 8 + [_vp] * 11 + [_vp] * 5 + [_i, _i, _vp]),
     "qwen35_b200_decode_steps": (_i, [C.POINTER(DecodeArgs), _vp]),
+    "qwen35_b200_decode_steps_nvfp4": (_i, [C.POINTER(DecodeArgs), _vp, _vp]),
+    "launch_decode_nvfp4": (_i, [_vp, _vp] + [_vp] * 5 + [_vp] * 4 + [_vp] * 5 + [_vp] * 10 + [_vp] * 5 + [_i, _i, _i, _vp]),
+    "launch_decode_many_nvfp4": (_i, [_vp, _vp, _i] + [_vp] * 5 + [_vp] * 4 + [_vp] * 5 + [_vp] * 10 + [_vp] * 5 + [_i, _i, _i, _vp]),
     "qwen35_b200_decode_steps_static": (_i, [C.POINTER(DecodeArgs), _vp]),
     "qwen35_b200_prefill_bf16": (_i, [C.POINTER(PrefillArgs), _vp]),
     "launch_prefill_bf16": (_i, [_vp, _i, _vp] + [_vp] * 5 + [_vp] * 4 + [_vp] * 3 + [_vp] * 5 + [_vp] * 5 + [_vp] * 4 + [_vp]),

@@ -120,6 +120,43 @@ def _quantize_matrix_nvfp4_tc(weight, padded_rows=None):
     return out
 
 
+def _attach_nvfp4_weights(weights, group_size=NVFP4_GROUP_SIZE, verbose=False):
+    """Quantise the decode-hot matrices (reference model.py:206-311): per layer qkv/z/out/gate/up/down (DeltaNet) or
+    q/k/v/o/gate/up/down (attention) in the decode-body layout, the LM head in the tensor-core layout."""
+    if "nvfp4" in weights and weights["nvfp4"]["group_size"] == group_size:
+        return weights
+    layers = []
+    for ld in weights["layer_data"]:
+        p = ld["ptrs"]
+        q = lambda t: _quantize_matrix_nvfp4(t, group_size)   # noqa: E731
+        if ld["type"] == 1:
+            qs = [q(p[1]), q(p[2]), q(p[3]), q(p[6]), q(p[8]), q(p[9]), q(p[10])]
+            ptrs = [p[0], qs[0]["packed"], qs[0]["scales"], qs[1]["packed"], qs[1]["scales"], qs[2]["packed"], qs[2]["scales"],
+                    p[4], p[5], qs[3]["packed"], qs[3]["scales"], p[7],
+                    qs[4]["packed"], qs[4]["scales"], qs[5]["packed"], qs[5]["scales"], qs[6]["packed"], qs[6]["scales"]]
+        else:
+            qs = [q(p[1]), q(p[2]), q(p[9]), q(p[11]), q(p[12]), q(p[13])]
+            ptrs = [p[0], qs[0]["packed"], qs[0]["scales"], qs[1]["packed"], qs[1]["scales"],
+                    p[3], p[4], p[5], p[6], p[7], p[8], qs[2]["packed"], qs[2]["scales"], p[10],
+                    qs[3]["packed"], qs[3]["scales"], qs[4]["packed"], qs[4]["scales"], qs[5]["packed"], qs[5]["scales"]]
+        layers.append({"type": ld["type"], "ptrs": ptrs, "quantized": qs})
+    lm = _quantize_matrix_nvfp4_lm(weights["lm_head_weight"])
+    weights["nvfp4"] = {"group_size": group_size, "lm_group_size": NVFP4_LM_GROUP_SIZE, "layer_data": layers,
+                        "lm_head_weight_packed": lm["packed"], "lm_head_scales": lm["scales"]}
+    return weights
+
+
+def _pack_layer_weights_nvfp4(layer_data, group_size, device="cuda"):
+    """Device blob of records {int type; int group_size; int pad[2]; void* ptrs[24]} (reference model.py:430-447)."""
+    rec = 16 + 24 * 8
+    buf = bytearray(len(layer_data) * rec)
+    for i, ld in enumerate(layer_data):
+        struct.pack_into("iiii", buf, i * rec, ld["type"], group_size, 0, 0)
+        for j, t in enumerate(ld["ptrs"]):
+            struct.pack_into("Q", buf, i * rec + 16 + j * 8, t.data_ptr())
+    return torch.frombuffer(buf, dtype=torch.uint8).to(device)
+
+
 DN_PROJ_FUSED_SIZE = DN_CONV_CHANNELS + DN_V_SIZE + 2 * DN_NUM_HEADS
 DN_PROJ_FUSED_PADDED_SIZE = ((DN_PROJ_FUSED_SIZE + 127) // 128) * 128
 PREFILL_PROJ_FUSED_SIZE = max(DN_PROJ_FUSED_PADDED_SIZE, FA_QPROJ_SIZE + 2 * FA_KV_SIZE, INTERMEDIATE_SIZE * 2)
@@ -171,10 +208,11 @@ class Decoder:
 
     def __init__(self, weights=None, tokenizer=None, model_name="random:1234", backend="bf16",
                  verbose=False, max_seq_len=MAX_SEQ_LEN, device="cuda"):
-        if backend not in ("bf16", "auto", None):
+        if backend not in ("bf16", "nvfp4", "auto", None):
             raise ValueError(f"unsupported backend: {backend}")
-        self.backend = "bf16"
-        self.backend_label = "BF16"
+        self.backend = "nvfp4" if backend == "nvfp4" else "bf16"
+        self.backend_label = "NVFP4 decode" if self.backend == "nvfp4" else "BF16"
+        self._nvfp4_group_size = NVFP4_GROUP_SIZE
         self._lib = _capi.lib()
         self.device = torch.device(device)
         if weights is None:
@@ -191,6 +229,13 @@ class Decoder:
         self._prefill_fused_weights_packed = _pack_prefill_fused_layer_weights(weights["prefill_fused_layer_data"], device)
         self._prefill_buffers = None
         self._prefill_buffer_tokens = 0
+        self._layer_weights_packed_nvfp4 = None
+        if self.backend == "nvfp4":
+            _attach_nvfp4_weights(weights, self._nvfp4_group_size)
+            nv = weights["nvfp4"]
+            self._layer_weights_packed_nvfp4 = _pack_layer_weights_nvfp4(nv["layer_data"], nv["group_size"], device)
+            self._lm_head_weight_packed = nv["lm_head_weight_packed"]
+            self._lm_head_scales = nv["lm_head_scales"]
 
         dev = self.device
         n_fa = sum(1 for t in LAYER_TYPE if t == 1)
@@ -228,7 +273,12 @@ class Decoder:
 
     def _run(self, a):
         with torch.cuda.device(self.device):
-            _capi.check(self._lib.qwen35_b200_decode_steps(C.byref(a), self._stream()), "decode")
+            if self.backend == "nvfp4":
+                a.layer_weights = self._layer_weights_packed_nvfp4.data_ptr()
+                a.lm_head_weight = self._lm_head_weight_packed.data_ptr()
+                _capi.check(self._lib.qwen35_b200_decode_steps_nvfp4(C.byref(a), self._lm_head_scales.data_ptr(), self._stream()), "decode_nvfp4")
+            else:
+                _capi.check(self._lib.qwen35_b200_decode_steps(C.byref(a), self._stream()), "decode")
 
     def check_status(self):
         """Synchronise and raise if a kernel recorded an error (e.g. a bounded wait ran out)."""
@@ -238,6 +288,10 @@ class Decoder:
     # ---- reference API -----------------------------------------------------------------------
     def step(self, token_id: int) -> int:
         """Decode one token, return the next token id (model.py:678-714; one D2H sync)."""
+        if self.backend == "nvfp4":
+            self._run(self._args(token_imm=int(token_id), n_steps=1))
+            self._position += 1
+            return int(self._out_token.item())
         with torch.cuda.device(self.device):
             none = None
             _capi.check(self._lib.launch_decode(

@@ -34,6 +34,15 @@ import torch
 import torch.nn.functional as F
 
 
+def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """Projection with f32 accumulation and one rounding to the activation dtype.  bf16 weights go through
+    F.linear (what a bf16 HuggingFace model does).  f32 weights are used for the NVFP4 variant, whose dequantised
+    values (E2M1 code x fp16 or E4M3 scale) are exact in f32 but not in bf16 (kernel_gb10_nvfp4.cu:521-545)."""
+    if w.dtype == x.dtype:
+        return F.linear(x, w)
+    return F.linear(x.float(), w.float()).to(x.dtype)
+
+
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     """x * rsqrt(mean x^2 + eps) * (1 + w), f32 math, one rounding to x.dtype
     (kernel.cu:173-260, `(1+w)` at :212)."""
@@ -180,10 +189,10 @@ class Oracle:
     def _deltanet(self, i_dn: int, p: list, x: torch.Tensor, use_state: bool) -> torch.Tensor:
         d = self.d
         S = x.shape[0]
-        mixed = F.linear(x, p[1]).transpose(0, 1)[None]          # [1, C, S]
-        z = F.linear(x, p[2]).reshape(S, d.dn_heads, d.dn_value_dim)
-        b = F.linear(x, p[3])
-        a = F.linear(x, p[4])
+        mixed = linear(x, p[1]).transpose(0, 1)[None]          # [1, C, S]
+        z = linear(x, p[2]).reshape(S, d.dn_heads, d.dn_value_dim)
+        b = linear(x, p[3])
+        a = linear(x, p[4])
         conv_w = p[5].squeeze(1)                                   # [C, 4]
         kw = d.dn_conv_kernel
         if use_state:
@@ -213,18 +222,18 @@ class Oracle:
             o, st = chunk_gated_delta_rule(q, k, v, g, beta, 64, None)
         self.dn_state[i_dn] = st.to(self.state_dtype)
         o = gated_rmsnorm(o.reshape(-1, d.dn_value_dim), z.reshape(-1, d.dn_value_dim), p[8], d.rms_eps)
-        return F.linear(o.reshape(S, -1), p[9])
+        return linear(o.reshape(S, -1), p[9])
 
     def _attention(self, i_fa: int, p: list, x: torch.Tensor, cos, sin) -> torch.Tensor:
         d = self.d
         S = x.shape[0]
         hd = d.fa_head_dim
-        qg = F.linear(x, p[1]).view(S, d.fa_q_heads, 2 * hd)
+        qg = linear(x, p[1]).view(S, d.fa_q_heads, 2 * hd)
         q, gate = torch.chunk(qg, 2, dim=-1)
         gate = gate.reshape(S, -1)
         q = rmsnorm(q, p[4], d.rms_eps).transpose(0, 1)                      # [Hq, S, hd]
-        k = rmsnorm(F.linear(x, p[2]).view(S, d.fa_kv_heads, hd), p[5], d.rms_eps).transpose(0, 1)
-        v = F.linear(x, p[3]).view(S, d.fa_kv_heads, hd).transpose(0, 1)
+        k = rmsnorm(linear(x, p[2]).view(S, d.fa_kv_heads, hd), p[5], d.rms_eps).transpose(0, 1)
+        v = linear(x, p[3]).view(S, d.fa_kv_heads, hd).transpose(0, 1)
         q = apply_rope(q, cos, sin)
         k = apply_rope(k, cos, sin)
         if self.k_cache[i_fa] is not None:
@@ -244,7 +253,7 @@ class Oracle:
         w = F.softmax(w, dim=-1, dtype=torch.float32).to(q.dtype)
         o = torch.matmul(w, vs).transpose(0, 1).contiguous().reshape(S, -1)
         o = o * torch.sigmoid(gate)
-        return F.linear(o, p[6])
+        return linear(o, p[6])
 
     def _forward(self, ids: torch.Tensor, use_state: bool) -> torch.Tensor:
         d = self.d
@@ -269,7 +278,7 @@ class Oracle:
                 post, gate_w, up_w, down_w = p[10], p[11], p[12], p[13]
             h = h + y
             x = rmsnorm(h, post, d.rms_eps)
-            h = h + F.linear(F.silu(F.linear(x, gate_w)) * F.linear(x, up_w), down_w)
+            h = h + linear(F.silu(linear(x, gate_w)) * linear(x, up_w), down_w)
             self.trace.append(h[-1])
         self.position += S
         self.last_hidden = h
@@ -279,7 +288,7 @@ class Oracle:
     @torch.no_grad()
     def logits_from_hidden(self, h: torch.Tensor) -> torch.Tensor:
         """Final RMSNorm + tied LM head; bf16 logits (kernel.cu:747-814 takes their arg-max)."""
-        return F.linear(rmsnorm(h, self.w["final_norm_weight"], self.d.rms_eps), self.w["lm_head_weight"])
+        return linear(rmsnorm(h, self.w["final_norm_weight"], self.d.rms_eps), self.w["lm_head_weight"])
 
     @torch.no_grad()
     def prefill(self, ids: torch.Tensor, all_logits: bool = False) -> torch.Tensor:
