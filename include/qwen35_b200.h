@@ -108,6 +108,19 @@ int launch_prefill_bf16(
     void* attn_buf, void* mlp_buf, void* dn_out_buf, void* beta_buf, void* alpha_buf,
     void* final_normed, void* hidden_bf16_out, void* lm_bmv, void* lm_bmi, qwen35_stream_t stream);
 
+/* Replaces launch_prefill_bf16_nvfp4_lm (torch_bindings.cpp:337-352): the same prefill with the last token's LM head read
+ * from the NVFP4 tensor-core layout.  The reference's activation quantisation buffers (lm_hidden_*, lm_logits_f16) are ignored. */
+int launch_prefill_bf16_nvfp4_lm(
+    const int* token_ids, int seq_len, int* output_token,
+    const void* embed_weight, const LayerWeights* layers, const void* fused_layers,
+    const void* final_norm_w, const void* lm_head_w, const void* lm_head_weight_packed, const void* lm_head_scales,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* hidden, void* residual, void* normalized,
+    void* proj_buf, void* proj_buf2, void* proj_buf_half, void* proj_act_packed, void* proj_act_scales,
+    void* attn_buf, void* mlp_buf, void* dn_out_buf, void* beta_buf, void* alpha_buf,
+    void* final_normed, void* hidden_bf16_out, void* lm_bmv, void* lm_bmi,
+    void* lm_hidden_bf16, void* lm_hidden_packed, void* lm_hidden_scales, void* lm_logits_f16, qwen35_stream_t stream);
+
 /* The same with an explicit cache length, optional logits and a layer limit for tests. */
 typedef struct {
     const int* token_ids; int seq_len; int* out_token;
@@ -131,6 +144,8 @@ typedef struct {
     float* logits_out;   /* optional f32 [248320] */
     int max_seq_len;
     int dbg_num_layers;  /* 0 = all */
+    const void* lm_head_weight_packed; /* optional: NVFP4 LM head (tensor-core layout) used for the last token */
+    const void* lm_head_scales;
 } Qwen35PrefillArgs;
 int qwen35_b200_prefill_bf16(const Qwen35PrefillArgs* args, qwen35_stream_t stream);
 

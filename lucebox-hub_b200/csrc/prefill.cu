@@ -52,6 +52,8 @@ struct PrefillArgs {
     bf16 *final_normed, *hidden_out;
     float* lm_bmv; int* lm_bmi;
     float* logits_out;
+    const void* lm_packed;     // optional NVFP4 LM head (tensor-core layout) for the last token
+    const void* lm_scales;
     int max_seq_len;
     int n_layers;
 };
@@ -126,7 +128,10 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
     if (a.hidden_out) Q35_CUDA_OK(cudaMemcpyAsync(a.hidden_out, last, HIDDEN * sizeof(bf16), cudaMemcpyDeviceToDevice, stream));
     pf_rmsnorm_kernel<<<1, 128, 0, stream>>>(nullptr, nullptr, last, a.final_norm, nullptr, a.final_normed, 1);
     const int lm_blocks = 592;
-    pf_lm_head_kernel<<<lm_blocks, 256, 0, stream>>>(a.final_normed, a.lm_head, a.lm_bmv, a.lm_bmi, a.logits_out);
+    if (a.lm_packed)
+        pf_lm_head_fp4_kernel<<<lm_blocks, 256, 0, stream>>>(a.final_normed, (const uint8_t*)a.lm_packed, (const uint8_t*)a.lm_scales, a.lm_bmv, a.lm_bmi, a.logits_out);
+    else
+        pf_lm_head_kernel<<<lm_blocks, 256, 0, stream>>>(a.final_normed, a.lm_head, a.lm_bmv, a.lm_bmi, a.logits_out);
     pf_lm_reduce_kernel<<<1, 32, 0, stream>>>(a.lm_bmv, a.lm_bmi, lm_blocks, a.out_token);
     g_launches.fetch_add(3);
     Q35_CUDA_OK(cudaGetLastError());
@@ -180,6 +185,7 @@ extern "C" int qwen35_b200_prefill_bf16(const Qwen35PrefillArgs* in, qwen35_stre
     a.dn_out_buf = (bf16*)in->dn_out_buf; a.beta_buf = (float*)in->beta_buf; a.alpha_buf = (float*)in->alpha_buf;
     a.final_normed = (bf16*)in->final_normed; a.hidden_out = (bf16*)in->hidden_bf16_out;
     a.lm_bmv = (float*)in->lm_bmv; a.lm_bmi = (int*)in->lm_bmi; a.logits_out = in->logits_out;
+    a.lm_packed = in->lm_head_weight_packed; a.lm_scales = in->lm_head_scales;
     a.max_seq_len = in->max_seq_len;
     a.n_layers = in->dbg_num_layers > 0 ? in->dbg_num_layers : NUM_LAYERS;
     return prefill_impl(a, (cudaStream_t)stream);
@@ -203,5 +209,30 @@ extern "C" int launch_prefill_bf16(
     a.attn_buf = attn_buf; a.mlp_buf = mlp_buf; a.dn_out_buf = dn_out_buf; a.beta_buf = beta_buf; a.alpha_buf = alpha_buf;
     a.final_normed = final_normed; a.hidden_bf16_out = hidden_bf16_out; a.lm_bmv = lm_bmv; a.lm_bmi = lm_bmi;
     a.max_seq_len = 2048;       // the reference's fixed cache length (prefill.cu:1203, 1394)
+    return qwen35_b200_prefill_bf16(&a, stream);
+}
+
+// Replaces launch_prefill_bf16_nvfp4_lm (torch_bindings.cpp:337-352; prefill.cu:1499-1534): the bf16 prefill body with the
+// NVFP4 LM head for the last token.
+extern "C" int launch_prefill_bf16_nvfp4_lm(
+    const int* token_ids, int seq_len, int* output_token,
+    const void* embed_weight, const LayerWeights* layers, const void* fused_layers,
+    const void* final_norm_w, const void* lm_head_w, const void* lm_head_weight_packed, const void* lm_head_scales,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* hidden, void* residual, void* normalized,
+    void* proj_buf, void* proj_buf2, void* /*proj_buf_half*/, void* /*proj_act_packed*/, void* /*proj_act_scales*/,
+    void* attn_buf, void* mlp_buf, void* dn_out_buf, void* beta_buf, void* alpha_buf,
+    void* final_normed, void* hidden_bf16_out, void* lm_bmv, void* lm_bmi,
+    void* /*lm_hidden_bf16*/, void* /*lm_hidden_packed*/, void* /*lm_hidden_scales*/, void* /*lm_logits_f16*/, qwen35_stream_t stream) {
+    Qwen35PrefillArgs a = {};
+    a.token_ids = token_ids; a.seq_len = seq_len; a.out_token = output_token;
+    a.embed_weight = embed_weight; a.layer_weights = layers; a.fused_layer_weights = fused_layers;
+    a.final_norm_weight = final_norm_w; a.lm_head_weight = lm_head_w;
+    a.lm_head_weight_packed = lm_head_weight_packed; a.lm_head_scales = lm_head_scales;
+    a.fa_k_cache = fa_k_cache; a.fa_v_cache = fa_v_cache; a.dn_states = dn_states; a.conv_bufs = conv_bufs;
+    a.hidden = hidden; a.residual = residual; a.normalized = normalized; a.proj_buf = proj_buf; a.proj_buf2 = proj_buf2;
+    a.attn_buf = attn_buf; a.mlp_buf = mlp_buf; a.dn_out_buf = dn_out_buf; a.beta_buf = beta_buf; a.alpha_buf = alpha_buf;
+    a.final_normed = final_normed; a.hidden_bf16_out = hidden_bf16_out; a.lm_bmv = lm_bmv; a.lm_bmi = lm_bmi;
+    a.max_seq_len = 2048;
     return qwen35_b200_prefill_bf16(&a, stream);
 }

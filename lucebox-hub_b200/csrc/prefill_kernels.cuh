@@ -10,6 +10,10 @@
 // Rounding points follow a bf16 HuggingFace model: every module output is rounded to bf16 once.
 #pragma once
 
+#include <cuda_fp16.h>
+#include <cuda_fp4.h>
+#include <cuda_fp8.h>
+
 #include "common.cuh"
 
 namespace q35 {
@@ -465,6 +469,54 @@ __global__ void __launch_bounds__(256) pf_lm_head_kernel(const bf16* __restrict_
     if (threadIdx.x == 0) {
         float bv = sv[0]; int bi = si[0];
         for (int w = 1; w < 8; ++w) if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+        bmv[blockIdx.x] = bv; bmi[blockIdx.x] = bi;
+    }
+}
+
+// NVFP4 LM head (tensor-core layout: packed E2M1 [V,512], E4M3 block scales in 128x4 swizzled tiles), one warp per row.
+// Reference: lm_head_kernel_nvfp4 (kernel_gb10_nvfp4.cu:1451-1523), the path its hybrid prefill ends with.
+__global__ void __launch_bounds__(256) pf_lm_head_fp4_kernel(const bf16* __restrict__ x, const uint8_t* __restrict__ packed,
+                                                             const uint8_t* __restrict__ scales, float* __restrict__ bmv, int* __restrict__ bmi,
+                                                             float* __restrict__ logits_out) {
+    __shared__ float sv[8];
+    __shared__ int si[8];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float xr[32];                                  // elements [32 lane, 32 lane + 32)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint4 v = *(reinterpret_cast<const uint4*>(x + 32 * lane) + j);
+        xr[8 * j + 0] = bf_lo(v.x); xr[8 * j + 1] = bf_hi(v.x); xr[8 * j + 2] = bf_lo(v.y); xr[8 * j + 3] = bf_hi(v.y);
+        xr[8 * j + 4] = bf_lo(v.z); xr[8 * j + 5] = bf_hi(v.z); xr[8 * j + 6] = bf_lo(v.w); xr[8 * j + 7] = bf_hi(v.w);
+    }
+    const int r0 = part_begin(VOCAB, blockIdx.x, gridDim.x), r1 = part_begin(VOCAB, blockIdx.x + 1, gridDim.x);
+    float best = -INFINITY;
+    int best_i = 0x7fffffff;
+    for (int r = r0 + warp; r < r1; r += 8) {
+        const uint4 pk = ld_stream(reinterpret_cast<const uint4*>(packed + (size_t)r * (HIDDEN / 2)) + lane);
+        const size_t tile = (size_t)(r >> 7) * (HIDDEN / 64) + (lane >> 1);
+        const unsigned short sraw = __ldg(reinterpret_cast<const unsigned short*>(scales + tile * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + ((2 * lane) & 3)));
+        const __half2_raw sh = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)sraw, __NV_E4M3);
+        const float2 sc = __half22float2(*reinterpret_cast<const __half2*>(&sh));
+        const uint32_t w[4] = {pk.x, pk.y, pk.z, pk.w};
+        float a[2] = {0.f, 0.f};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int bb = 0; bb < 4; ++bb) {
+                const __half2_raw h = __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)((w[i] >> (8 * bb)) & 0xffu), __NV_E2M1);
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+                a[i >> 1] = fmaf(f.x, xr[i * 8 + bb * 2], a[i >> 1]);
+                a[i >> 1] = fmaf(f.y, xr[i * 8 + bb * 2 + 1], a[i >> 1]);
+            }
+        const float v = rbf(warp_sum(a[0] * sc.x + a[1] * sc.y));
+        if (lane == 0 && logits_out) logits_out[r] = v;
+        if (v > best) { best = v; best_i = r; }
+    }
+    if (lane == 0) { sv[warp] = best; si[warp] = best_i; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float bv = sv[0]; int bi = si[0];
+        for (int w2 = 1; w2 < 8; ++w2) if (sv[w2] > bv || (sv[w2] == bv && si[w2] < bi)) { bv = sv[w2]; bi = si[w2]; }
         bmv[blockIdx.x] = bv; bmi[blockIdx.x] = bi;
     }
 }

@@ -42,6 +42,7 @@ class PrefillArgs(C.Structure):
         ("dn_out_buf", C.c_void_p), ("beta_buf", C.c_void_p), ("alpha_buf", C.c_void_p),
         ("final_normed", C.c_void_p), ("hidden_bf16_out", C.c_void_p), ("lm_bmv", C.c_void_p), ("lm_bmi", C.c_void_p),
         ("logits_out", C.c_void_p), ("max_seq_len", C.c_int), ("dbg_num_layers", C.c_int),
+        ("lm_head_weight_packed", C.c_void_p), ("lm_head_scales", C.c_void_p),
     ]
 
 
@@ -57,6 +58,7 @@ SIGNATURES = {
     "launch_decode_many_nvfp4": (_i, [_vp, _vp, _i] + [_vp] * 5 + [_vp] * 4 + [_vp] * 5 + [_vp] * 10 + [_vp] * 5 + [_i, _i, _i, _vp]),
     "qwen35_b200_decode_steps_static": (_i, [C.POINTER(DecodeArgs), _vp]),
     "qwen35_b200_prefill_bf16": (_i, [C.POINTER(PrefillArgs), _vp]),
+    "launch_prefill_bf16_nvfp4_lm": (_i, [_vp, _i, _vp] + [_vp] * 7 + [_vp] * 4 + [_vp] * 3 + [_vp] * 5 + [_vp] * 5 + [_vp] * 4 + [_vp] * 4 + [_vp]),
     "launch_prefill_bf16": (_i, [_vp, _i, _vp] + [_vp] * 5 + [_vp] * 4 + [_vp] * 3 + [_vp] * 5 + [_vp] * 5 + [_vp] * 4 + [_vp]),
     "launch_quantize_nvfp4_out": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp]),
     "launch_quantize_nvfp4_lm_out": (_i, [_vp, _i, _i, _vp, _vp, _vp]),
