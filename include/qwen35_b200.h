@@ -191,6 +191,27 @@ int launch_quantize_nvfp4_out(const void* weight, int rows, int cols, int group_
  * scale 1.0.  rows must be a multiple of 128 and cols a multiple of 64. */
 int launch_quantize_nvfp4_lm_out(const void* weight, int rows, int cols, void* packed_out, void* scales_out, qwen35_stream_t stream);
 
+/* Batched greedy decode (no counterpart in the reference, which is batch-1 only: README.md:167): `batch`
+ * independent sequences advance one token.  Each sequence follows the bs=1 arithmetic of launch_decode.
+ *   tokens_in / tokens_out  int32 [batch]            positions  int32 [batch] tokens already cached per sequence
+ *   k_pages / v_pages       bf16 [6][num_pages][2][64][256], addressed through block_table int32 [batch][max_pages]
+ *   dn_states f32 [batch][18][16][128][128]          conv_bufs f32 [batch][18][6144][4]
+ * max_ctx bounds positions+1 (<= 8192).  advance_positions != 0 increments positions[] on the device after the
+ * step, so steps chain without host work.  Weights are the bf16 tables of launch_prefill_bf16. */
+typedef struct {
+    int batch; int max_ctx; int num_pages; int max_pages;
+    const int* tokens_in; int* tokens_out; int* positions; const int* block_table;
+    const void* embed_weight; const LayerWeights* layer_weights; const void* fused_layer_weights;
+    const void* final_norm_weight; const void* lm_head_weight;
+    void* k_pages; void* v_pages; void* dn_states; void* conv_bufs;
+    void* logits_out;          /* optional bf16 [batch][248320] */
+    void* dbg_hidden;          /* optional bf16 [24][batch][1024]: every layer's output */
+    const void* dbg_teacher;   /* optional bf16 [24][batch][1024]: layer l>0 reads row block l as its input */
+    int advance_positions;
+    int dbg_num_layers;
+} Qwen35BatchedArgs;
+int qwen35_b200_decode_batched(const Qwen35BatchedArgs* args, qwen35_stream_t stream);
+
 /* BF16 GEMM on tcgen05/TMEM tensor cores: C[M,N] = epi(A[M,K] . B[b_rows,K]^T), f32 accumulate, one
  * rounding to bf16.  Replaces cublas_bf16_gemm (prefill.cu:895-903).  lda/ldc/ldr are row strides in
  * elements; K must be a multiple of 64.  epilogue: 0 = store, 1 = + R (residual, bf16 add),

@@ -1,0 +1,382 @@
+// Batched greedy decode: B independent sequences per GPU advance one token per call, weights read once per
+// step for all of them.  The reference is batch-1 only (models/qwen35_0p8b/README.md:167); this is the
+// additive op its benchmark configuration "64 sequences per GPU, 2048-token contexts" needs.  Every sequence
+// follows exactly the bs=1 arithmetic of the decode megakernel (kernel.cu:409-741 restated), so the CPU oracle
+// for a sequence is the bs=1 oracle.
+//
+// One step = a short stream of kernels (no host synchronisation, capturable in a CUDA graph):
+//   per layer  RMSNorm rows -> projection GEMM (tcgen05, M = B) -> DeltaNet step (conv + SiLU, L2 norm,
+//              recurrence on the f32 state of every (sequence, head)) + conv shift + gated norm, or q/k norm +
+//              RoPE + paged KV append + attention over the paged bf16 KV cache -> output GEMM + residual ->
+//              RMSNorm -> gate/up GEMM with fused SiLU*up -> down GEMM + residual
+//   finally    RMSNorm -> LM-head GEMM [B, 248320] -> per-row arg-max (lowest index among equal bf16 maxima)
+// KV cache pages: [layer 6][page][kv head 2][64 positions][256] bf16, addressed through block_table[B][max_pages].
+#include "prefill_kernels.cuh"
+
+#include <cmath>
+#include <mutex>
+
+#include "runtime.h"
+
+namespace q35 {
+
+int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ldc, const bf16* R, int ldr,
+              int M, int N, int K, int epi, int up_row_offset, cudaStream_t stream);
+
+constexpr int KV_PAGE = 64;
+
+__device__ __forceinline__ float conv_silu4(const bf16* conv_w, int ch, float4 st, float x) {
+    const uint2 wr = __ldg(reinterpret_cast<const uint2*>(conv_w) + ch);
+    float c = bf_lo(wr.x) * st.y;
+    c = fmaf(bf_hi(wr.x), st.z, c);
+    c = fmaf(bf_lo(wr.y), st.w, c);
+    c = fmaf(bf_hi(wr.y), x, c);
+    return rbf(silu_f(rbf(c)));
+}
+
+// ---- DeltaNet step: one CTA (128 threads) per (sequence, head, block of 16 value rows) ------------------
+__global__ void __launch_bounds__(128) bd_dn_step_kernel(const bf16* __restrict__ proj, int ldp, const bf16* __restrict__ conv_w,
+                                                         const bf16* __restrict__ a_log, const bf16* __restrict__ dt_bias,
+                                                         const float* __restrict__ conv, size_t conv_seq_stride,
+                                                         float* __restrict__ state, size_t state_seq_stride, bf16* __restrict__ core_out) {
+    __shared__ __align__(16) float sq[DN_K];
+    __shared__ __align__(16) float sk[DN_K];
+    __shared__ float red[2][4];
+    __shared__ float shd[2];
+    const int b = blockIdx.x, h = blockIdx.y, rb = blockIdx.z, i = threadIdx.x, warp = i >> 5, lane = i & 31;
+    const bf16* xrow = proj + (size_t)b * ldp;
+    const float4* cv = reinterpret_cast<const float4*>(conv + (size_t)b * conv_seq_stride);
+    // q and k of this head: conv + SiLU, then the L2 norm in bf16 arithmetic (single-token form of the oracle)
+    const int chq = h * DN_K + i, chk = DN_QK_SIZE + h * DN_K + i;
+    const float cq = conv_silu4(conv_w, chq, cv[chq], bf2f(xrow[chq]));
+    const float ck = conv_silu4(conv_w, chk, cv[chk], bf2f(xrow[chk]));
+    const float s0 = warp_sum(rbf(cq * cq)), s1 = warp_sum(rbf(ck * ck));
+    if (lane == 0) { red[0][warp] = s0; red[1][warp] = s1; }
+    if (i == 0) {
+        const float bb = bf2f(xrow[DN_CONV_CH + DN_V_SIZE + h]);
+        const float aa = bf2f(xrow[DN_CONV_CH + DN_V_SIZE + DN_HEADS + h]);
+        const float x = aa + bf2f(dt_bias[h]);
+        const float sp = (x > 20.f) ? x : log1pf(expf(x));
+        shd[0] = rbf(sigmoid_f(bb));
+        shd[1] = expf(-expf(bf2f(a_log[h])) * sp);
+    }
+    __syncthreads();
+    {
+        float tq = ((red[0][0] + red[0][1]) + red[0][2]) + red[0][3];
+        float tk = ((red[1][0] + red[1][1]) + red[1][2]) + red[1][3];
+        tq = rbf(rbf(tq) + 1e-6f);
+        tk = rbf(rbf(tk) + 1e-6f);
+        sq[i] = rbf(cq * rbf(1.0f / rbf(sqrtf(tq)))) * 0.08838834764831845f;
+        sk[i] = rbf(ck * rbf(1.0f / rbf(sqrtf(tk))));
+    }
+    __syncthreads();
+    const float4 q4 = *reinterpret_cast<const float4*>(&sq[lane * 4]);
+    const float4 k4 = *reinterpret_cast<const float4*>(&sk[lane * 4]);
+    const float beta = shd[0], decay = shd[1];
+    float* st_base = state + (size_t)b * state_seq_stride + (size_t)h * DN_V * DN_K;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const int v = rb * 16 + warp * 4 + r;
+        const int ch = 2 * DN_QK_SIZE + h * DN_V + v;
+        const float vv = conv_silu4(conv_w, ch, cv[ch], bf2f(xrow[ch]));
+        float4* sp = reinterpret_cast<float4*>(st_base + (size_t)v * DN_K) + lane;
+        float4 t = *sp;
+        t.x = __fmul_rn(t.x, decay); t.y = __fmul_rn(t.y, decay); t.z = __fmul_rn(t.z, decay); t.w = __fmul_rn(t.w, decay);
+        float kv = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(t.x, k4.x), __fmul_rn(t.y, k4.y)), __fmul_rn(t.z, k4.z)), __fmul_rn(t.w, k4.w));
+        kv = warp_sum(kv);
+        const float delta = __fmul_rn(__fsub_rn(vv, kv), beta);
+        t.x = __fadd_rn(t.x, __fmul_rn(k4.x, delta)); t.y = __fadd_rn(t.y, __fmul_rn(k4.y, delta));
+        t.z = __fadd_rn(t.z, __fmul_rn(k4.z, delta)); t.w = __fadd_rn(t.w, __fmul_rn(k4.w, delta));
+        float o = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(t.x, q4.x), __fmul_rn(t.y, q4.y)), __fmul_rn(t.z, q4.z)), __fmul_rn(t.w, q4.w));
+        o = warp_sum(o);
+        *sp = t;
+        if (lane == 0) core_out[(size_t)b * DN_V_SIZE + h * DN_V + v] = f2bf(o);
+    }
+}
+
+// conv window shift for every (sequence, channel), after all readers of the old window have finished
+__global__ void bd_conv_shift_kernel(const bf16* __restrict__ proj, int ldp, float* __restrict__ conv, size_t conv_seq_stride, int B) {
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= B * DN_CONV_CH) return;
+    const int b = idx / DN_CONV_CH, ch = idx % DN_CONV_CH;
+    float4* p = reinterpret_cast<float4*>(conv + (size_t)b * conv_seq_stride) + ch;
+    const float4 s = *p;
+    *p = make_float4(s.y, s.z, s.w, bf2f(proj[(size_t)b * ldp + ch]));
+}
+
+__device__ __forceinline__ bf16* kv_row(bf16* pages, const int* table, int max_pages, int b, int kvh, int pos) {
+    const int page = table[b * max_pages + pos / KV_PAGE];
+    return pages + (((size_t)page * FA_KV_HEADS + kvh) * KV_PAGE + (pos % KV_PAGE)) * FA_HEAD_DIM;
+}
+
+// ---- attention preparation: one warp per (sequence, slot); slots 0-7 q heads, 8-9 k heads, 10-11 v heads ----
+__global__ void __launch_bounds__(256) bd_qk_norm_rope_kernel(const bf16* __restrict__ proj, int ldp, const bf16* __restrict__ qn_w,
+                                                              const bf16* __restrict__ kn_w, const RopeTable inv_freq,
+                                                              const int* __restrict__ positions, const int* __restrict__ table, int max_pages,
+                                                              bf16* __restrict__ q_out, bf16* __restrict__ k_pages, bf16* __restrict__ v_pages, int B) {
+    const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (gw >= B * 12) return;
+    const int b = gw / 12, slot = gw % 12, pos = positions[b];
+    if (slot >= 10) {
+        const int kvh = slot - 10;
+        const uint4 v = *(reinterpret_cast<const uint4*>(proj + (size_t)b * ldp + FA_QPROJ + FA_KV_SIZE + kvh * FA_HEAD_DIM) + lane);
+        *(reinterpret_cast<uint4*>(kv_row(v_pages, table, max_pages, b, kvh, pos)) + lane) = v;
+        return;
+    }
+    const bool isq = slot < 8;
+    const bf16* src = proj + (size_t)b * ldp + (isq ? slot * 2 * FA_HEAD_DIM : FA_QPROJ + (slot - 8) * FA_HEAD_DIM);
+    const bf16* nw = isq ? qn_w : kn_w;
+    float xv[8], ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { xv[i] = bf2f(src[lane + 32 * i]); ss += xv[i] * xv[i]; }
+    const float r = rsqrt_ieee(warp_sum(ss) * (1.0f / FA_HEAD_DIM) + RMS_EPS);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xv[i] = rbf((xv[i] * r) * (1.0f + bf2f(nw[lane + 32 * i])));
+    const float ang = (float)pos * inv_freq.f[lane];
+    const float cs = rbf(cosf(ang)), sn = rbf(sinf(ang));
+    const float x1 = xv[0], x2 = xv[1];
+    xv[0] = rbf(rbf(x1 * cs) + rbf(-x2 * sn));
+    xv[1] = rbf(rbf(x2 * cs) + rbf(x1 * sn));
+    bf16* dst = isq ? q_out + (size_t)b * FA_Q_SIZE + slot * FA_HEAD_DIM : kv_row(k_pages, table, max_pages, b, slot - 8, pos);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dst[lane + 32 * i] = f2bf(xv[i]);
+}
+
+// ---- decode attention over the paged cache: one warp per (sequence, q head), exact bf16 rounding points ----
+constexpr int BD_ATT_WARPS = 4;
+__global__ void __launch_bounds__(BD_ATT_WARPS * 32) bd_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k_pages,
+                                                                         const bf16* __restrict__ v_pages, const int* __restrict__ positions,
+                                                                         const int* __restrict__ table, int max_pages, const bf16* __restrict__ proj,
+                                                                         int ldp, bf16* __restrict__ out, int B, int max_ctx) {
+    extern __shared__ float bd_sm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gw = blockIdx.x * BD_ATT_WARPS + warp;
+    if (gw >= B * FA_Q_HEADS) return;
+    const int b = gw / FA_Q_HEADS, head = gw % FA_Q_HEADS, kvh = head / FA_GQA;
+    float* sc = bd_sm + (size_t)warp * max_ctx;
+    float* sqv = bd_sm + (size_t)BD_ATT_WARPS * max_ctx + warp * FA_HEAD_DIM;
+    const int L = positions[b] + 1;
+    for (int i = lane; i < FA_HEAD_DIM; i += 32) sqv[i] = bf2f(q[(size_t)b * FA_Q_SIZE + head * FA_HEAD_DIM + i]);
+    __syncwarp();
+    const int* tb = table + b * max_pages;
+    float mx = -INFINITY;
+    for (int j = lane; j < L; j += 32) {
+        const uint4* kr = reinterpret_cast<const uint4*>(k_pages + (((size_t)tb[j / KV_PAGE] * FA_KV_HEADS + kvh) * KV_PAGE + (j % KV_PAGE)) * FA_HEAD_DIM);
+        float d = 0.f;
+#pragma unroll 4
+        for (int c = 0; c < FA_HEAD_DIM / 8; ++c) {
+            const uint4 kv = kr[c];
+            const float* qq = sqv + c * 8;
+            d = fmaf(qq[0], bf_lo(kv.x), d); d = fmaf(qq[1], bf_hi(kv.x), d);
+            d = fmaf(qq[2], bf_lo(kv.y), d); d = fmaf(qq[3], bf_hi(kv.y), d);
+            d = fmaf(qq[4], bf_lo(kv.z), d); d = fmaf(qq[5], bf_hi(kv.z), d);
+            d = fmaf(qq[6], bf_lo(kv.w), d); d = fmaf(qq[7], bf_hi(kv.w), d);
+        }
+        const float s = rbf(d) * 0.0625f;
+        sc[j] = s;
+        mx = fmaxf(mx, s);
+    }
+    mx = warp_max(mx);
+    float sm = 0.f;
+    for (int j = lane; j < L; j += 32) sm += expf(sc[j] - mx);
+    sm = warp_sum(sm);
+    for (int j = lane; j < L; j += 32) sc[j] = rbf(expf(sc[j] - mx) / sm);
+    __syncwarp();
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < L; ++j) {
+        const float p = sc[j];
+        const uint4 vv = *(reinterpret_cast<const uint4*>(v_pages + (((size_t)tb[j / KV_PAGE] * FA_KV_HEADS + kvh) * KV_PAGE + (j % KV_PAGE)) * FA_HEAD_DIM) + lane);
+        acc[0] = fmaf(p, bf_lo(vv.x), acc[0]); acc[1] = fmaf(p, bf_hi(vv.x), acc[1]);
+        acc[2] = fmaf(p, bf_lo(vv.y), acc[2]); acc[3] = fmaf(p, bf_hi(vv.y), acc[3]);
+        acc[4] = fmaf(p, bf_lo(vv.z), acc[4]); acc[5] = fmaf(p, bf_hi(vv.z), acc[5]);
+        acc[6] = fmaf(p, bf_lo(vv.w), acc[6]); acc[7] = fmaf(p, bf_hi(vv.w), acc[7]);
+    }
+    const uint4 gr = *(reinterpret_cast<const uint4*>(proj + (size_t)b * ldp + head * 2 * FA_HEAD_DIM + FA_HEAD_DIM) + lane);
+    const float gv[8] = {bf_lo(gr.x), bf_hi(gr.x), bf_lo(gr.y), bf_hi(gr.y), bf_lo(gr.z), bf_hi(gr.z), bf_lo(gr.w), bf_hi(gr.w)};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat162 pr = __halves2bfloat162(f2bf(rbf(acc[2 * i]) * rbf(sigmoid_f(gv[2 * i]))),
+                                                     f2bf(rbf(acc[2 * i + 1]) * rbf(sigmoid_f(gv[2 * i + 1]))));
+        o[i] = *reinterpret_cast<const uint32_t*>(&pr);
+    }
+    *(reinterpret_cast<uint4*>(out + (size_t)b * FA_Q_SIZE + head * FA_HEAD_DIM) + lane) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// ---- per-row arg-max over bf16 logits [B, VOCAB]: one CTA per row ---------------------------------------
+__global__ void __launch_bounds__(1024) bd_argmax_kernel(const bf16* __restrict__ logits, int* __restrict__ out_tokens, int* __restrict__ positions) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const int b = blockIdx.x, tid = threadIdx.x;
+    const uint4* row = reinterpret_cast<const uint4*>(logits + (size_t)b * VOCAB);
+    float best = -INFINITY;
+    int best_i = 0x7fffffff;
+    for (int c = tid; c < VOCAB / 8; c += 1024) {
+        const uint4 v = row[c];
+        const float f[8] = {bf_lo(v.x), bf_hi(v.x), bf_lo(v.y), bf_hi(v.y), bf_lo(v.z), bf_hi(v.z), bf_lo(v.w), bf_hi(v.w)};
+#pragma unroll
+        for (int k = 0; k < 8; ++k) if (f[k] > best) { best = f[k]; best_i = c * 8 + k; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float v = __shfl_xor_sync(0xffffffffu, best, o); const int k = __shfl_xor_sync(0xffffffffu, best_i, o);
+        if (v > best || (v == best && k < best_i)) { best = v; best_i = k; }
+    }
+    if ((tid & 31) == 0) { sv[tid >> 5] = best; si[tid >> 5] = best_i; }
+    __syncthreads();
+    if (tid < 32) {
+        best = sv[tid]; best_i = si[tid];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float v = __shfl_xor_sync(0xffffffffu, best, o); const int k = __shfl_xor_sync(0xffffffffu, best_i, o);
+            if (v > best || (v == best && k < best_i)) { best = v; best_i = k; }
+        }
+        if (tid == 0) { out_tokens[b] = best_i; if (positions) positions[b] += 1; }
+    }
+}
+
+// debug / teacher forcing helpers
+__global__ void bd_copy_rows_kernel(const bf16* __restrict__ src, bf16* __restrict__ dst, int n_u4) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n_u4) reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+}
+
+static void* g_bscratch[64] = {};
+static size_t g_bscratch_bytes[64] = {};
+static std::mutex g_bscratch_mu;
+
+static void* batched_scratch(size_t bytes) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    dev &= 63;
+    std::lock_guard<std::mutex> lk(g_bscratch_mu);
+    if (g_bscratch_bytes[dev] < bytes) {
+        if (g_bscratch[dev]) { cudaDeviceSynchronize(); cudaFree(g_bscratch[dev]); g_bscratch[dev] = nullptr; g_bscratch_bytes[dev] = 0; }
+        if (cudaMalloc(&g_bscratch[dev], bytes) != cudaSuccess) { set_error("batched decode scratch allocation of %zu bytes failed", bytes); return nullptr; }
+        g_bscratch_bytes[dev] = bytes;
+    }
+    return g_bscratch[dev];
+}
+
+struct PrefillFusedB { const void* proj_weight; const void* gate_up_weight; const void* unused[4]; };
+struct HostTablesB { const void* dev_layers; const void* dev_fused; LayerRec layers[NUM_LAYERS]; PrefillFusedB fused[NUM_LAYERS]; };
+static HostTablesB g_btables[8];
+static int g_btables_n = 0;
+static std::mutex g_btables_mu;
+
+static const HostTablesB* host_tables_b(const void* dev_layers, const void* dev_fused) {
+    std::lock_guard<std::mutex> lk(g_btables_mu);
+    for (int i = 0; i < g_btables_n; ++i)
+        if (g_btables[i].dev_layers == dev_layers && g_btables[i].dev_fused == dev_fused) return &g_btables[i];
+    HostTablesB* t = &g_btables[g_btables_n < 8 ? g_btables_n++ : 7];
+    t->dev_layers = dev_layers; t->dev_fused = dev_fused;
+    if (cudaMemcpy(t->layers, dev_layers, sizeof(t->layers), cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemcpy(t->fused, dev_fused, sizeof(t->fused), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        set_error("reading the layer tables failed");
+        t->dev_layers = nullptr;
+        return nullptr;
+    }
+    return t;
+}
+
+}  // namespace q35
+
+#define Q35_TRYB(expr)                       \
+    do {                                     \
+        const int st__ = (expr);             \
+        if (st__ != QWEN35_OK) return st__;  \
+    } while (0)
+
+extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_stream_t stream_) {
+    using namespace q35;
+    cudaStream_t stream = (cudaStream_t)stream_;
+    if (!in) { set_error("null args"); return QWEN35_ERR_BAD_ARG; }
+    const int B = in->batch;
+    if (B <= 0 || B > 1024 || in->max_ctx <= 0 || in->max_ctx > 8192 || in->max_pages * KV_PAGE < in->max_ctx) {
+        set_error("batched decode: batch %d, max_ctx %d, max_pages %d out of range (batch <= 1024, max_ctx <= 8192 <= max_pages*64)", B, in->max_ctx, in->max_pages);
+        return QWEN35_ERR_BAD_ARG;
+    }
+    if (!in->tokens_in || !in->tokens_out || !in->positions || !in->block_table || !in->k_pages || !in->v_pages || !in->dn_states || !in->conv_bufs ||
+        !in->embed_weight || !in->layer_weights || !in->fused_layer_weights || !in->lm_head_weight || !in->final_norm_weight) {
+        set_error("null tensor pointer");
+        return QWEN35_ERR_BAD_ARG;
+    }
+    const HostTablesB* t = host_tables_b(in->layer_weights, in->fused_layer_weights);
+    if (!t) return QWEN35_ERR_CUDA;
+    static bool attr_done = false;
+    if (!attr_done) {
+        Q35_CUDA_OK(cudaFuncSetAttribute(bd_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)((BD_ATT_WARPS * 8192 + BD_ATT_WARPS * FA_HEAD_DIM) * sizeof(float))));
+        attr_done = true;
+    }
+    // scratch rows of B tokens
+    const size_t rows = (size_t)B;
+    const size_t n_hidden = rows * HIDDEN, n_proj = rows * DN_PROJ_ROWS, n_att = rows * 2048, n_mlp = rows * INTER, n_logits = rows * VOCAB;
+    const size_t total = (3 * n_hidden + n_proj + 3 * n_att + n_mlp + n_logits) * sizeof(bf16) + 4096;
+    char* base = (char*)batched_scratch(total);
+    if (!base) return QWEN35_ERR_CUDA;
+    bf16* hidden = (bf16*)base;
+    bf16* resid = hidden + n_hidden;
+    bf16* normed = resid + n_hidden;
+    bf16* proj = normed + n_hidden;
+    bf16* qbuf = proj + n_proj;
+    bf16* core = qbuf + n_att;
+    bf16* attn = core + n_att;
+    bf16* mlp = attn + n_att;
+    bf16* logits = mlp + n_mlp;
+    RopeTable rt;
+    for (int i = 0; i < FA_ROT / 2; ++i) rt.f[i] = 1.0f / (float)std::pow(1.0e7, (double)((float)(2 * i) / (float)FA_ROT));
+    const size_t conv_stride = (size_t)N_DN * DN_CONV_CH * 4, state_stride = (size_t)N_DN * DN_HEADS * DN_V * DN_K;
+    const int n_layers = in->dbg_num_layers > 0 ? in->dbg_num_layers : NUM_LAYERS;
+    const size_t page_layer_stride = (size_t)in->num_pages * FA_KV_HEADS * KV_PAGE * FA_HEAD_DIM;
+
+    int i_dn = 0, i_fa = 0;
+    for (int layer = 0; layer < n_layers; ++layer) {
+        const LayerRec& L = t->layers[layer];
+        const PrefillFusedB& F = t->fused[layer];
+        if (layer > 0 && in->dbg_teacher)
+            bd_copy_rows_kernel<<<(int)((n_hidden / 8 + 255) / 256), 256, 0, stream>>>((const bf16*)in->dbg_teacher + (size_t)layer * n_hidden, hidden, (int)(n_hidden / 8));
+        pf_rmsnorm_kernel<<<B, 128, 0, stream>>>(layer == 0 ? in->tokens_in : nullptr, (const bf16*)in->embed_weight, hidden, (const bf16*)L.p[0],
+                                                 layer == 0 ? hidden : nullptr, normed, B);
+        const bf16 *w_out, *w_post, *w_down;
+        if (L.type == 0) {
+            const int ldp = DN_PROJ_ROWS;
+            Q35_TRYB(gemm_bf16(normed, HIDDEN, (const bf16*)F.proj_weight, DN_PROJ_ROWS, proj, ldp, nullptr, 0, B, DN_PROJ_ROWS, HIDDEN, 0, 0, stream));
+            float* conv = (float*)in->conv_bufs + (size_t)i_dn * DN_CONV_CH * 4;
+            float* state = (float*)in->dn_states + (size_t)i_dn * DN_HEADS * DN_V * DN_K;
+            bd_dn_step_kernel<<<dim3(B, DN_HEADS, DN_V / 16), 128, 0, stream>>>(proj, ldp, (const bf16*)L.p[DN_CONV], (const bf16*)L.p[DN_ALOG],
+                                                                                  (const bf16*)L.p[DN_DTBIAS], conv, conv_stride, state, state_stride, core);
+            bd_conv_shift_kernel<<<(B * DN_CONV_CH + 255) / 256, 256, 0, stream>>>(proj, ldp, conv, conv_stride, B);
+            pf_gated_norm_kernel<<<(B * DN_HEADS + 7) / 8, 256, 0, stream>>>(core, proj, ldp, (const bf16*)L.p[DN_NORM], attn, B);
+            g_launches.fetch_add(3);
+            w_out = (const bf16*)L.p[DN_OUT]; w_post = (const bf16*)L.p[DN_POST_NORM]; w_down = (const bf16*)L.p[DN_DOWN];
+            ++i_dn;
+        } else {
+            const int ldp = FA_PROJ_ROWS;
+            Q35_TRYB(gemm_bf16(normed, HIDDEN, (const bf16*)F.proj_weight, FA_PROJ_ROWS, proj, ldp, nullptr, 0, B, FA_PROJ_ROWS, HIDDEN, 0, 0, stream));
+            bf16* kp = (bf16*)in->k_pages + (size_t)i_fa * page_layer_stride;
+            bf16* vp = (bf16*)in->v_pages + (size_t)i_fa * page_layer_stride;
+            bd_qk_norm_rope_kernel<<<(B * 12 + 7) / 8, 256, 0, stream>>>(proj, ldp, (const bf16*)L.p[FA_QNORM], (const bf16*)L.p[FA_KNORM], rt,
+                                                                         in->positions, in->block_table, in->max_pages, qbuf, kp, vp, B);
+            const size_t smem = ((size_t)BD_ATT_WARPS * in->max_ctx + BD_ATT_WARPS * FA_HEAD_DIM) * sizeof(float);
+            bd_attention_kernel<<<(B * FA_Q_HEADS + BD_ATT_WARPS - 1) / BD_ATT_WARPS, BD_ATT_WARPS * 32, smem, stream>>>(
+                qbuf, kp, vp, in->positions, in->block_table, in->max_pages, proj, ldp, attn, B, in->max_ctx);
+            g_launches.fetch_add(2);
+            w_out = (const bf16*)L.p[FA_O]; w_post = (const bf16*)L.p[FA_POST_NORM]; w_down = (const bf16*)L.p[FA_DOWN];
+            ++i_fa;
+        }
+        Q35_TRYB(gemm_bf16(attn, 2048, w_out, HIDDEN, resid, HIDDEN, hidden, HIDDEN, B, HIDDEN, 2048, 1, 0, stream));
+        pf_rmsnorm_kernel<<<B, 128, 0, stream>>>(nullptr, nullptr, resid, w_post, nullptr, normed, B);
+        Q35_TRYB(gemm_bf16(normed, HIDDEN, (const bf16*)F.gate_up_weight, 2 * INTER, mlp, INTER, nullptr, 0, B, INTER, HIDDEN, 2, INTER, stream));
+        Q35_TRYB(gemm_bf16(mlp, INTER, w_down, HIDDEN, hidden, HIDDEN, resid, HIDDEN, B, HIDDEN, INTER, 1, 0, stream));
+        g_launches.fetch_add(2);
+        if (in->dbg_hidden)
+            bd_copy_rows_kernel<<<(int)((n_hidden / 8 + 255) / 256), 256, 0, stream>>>(hidden, (bf16*)in->dbg_hidden + (size_t)layer * n_hidden, (int)(n_hidden / 8));
+    }
+    pf_rmsnorm_kernel<<<B, 128, 0, stream>>>(nullptr, nullptr, hidden, (const bf16*)in->final_norm_weight, nullptr, normed, B);
+    Q35_TRYB(gemm_bf16(normed, HIDDEN, (const bf16*)in->lm_head_weight, VOCAB, logits, VOCAB, nullptr, 0, B, VOCAB, HIDDEN, 0, 0, stream));
+    bd_argmax_kernel<<<B, 1024, 0, stream>>>(logits, in->tokens_out, in->advance_positions ? in->positions : nullptr);
+    if (in->logits_out) Q35_CUDA_OK(cudaMemcpyAsync(in->logits_out, logits, n_logits * sizeof(bf16), cudaMemcpyDeviceToDevice, stream));
+    g_launches.fetch_add(2);
+    Q35_CUDA_OK(cudaGetLastError());
+    return QWEN35_OK;
+}

@@ -22,7 +22,7 @@ constexpr int DN_CHUNK = 64;
 
 // ---- one CTA (128 threads) per token: optional embedding gather, RMSNorm(1+w) -------------------
 // h_out (may be null) receives the raw row; x_out the normalised row.
-__global__ void __launch_bounds__(128) pf_rmsnorm_kernel(const int* __restrict__ ids, const bf16* __restrict__ embed,
+static __global__ void __launch_bounds__(128) pf_rmsnorm_kernel(const int* __restrict__ ids, const bf16* __restrict__ embed,
                                                          const bf16* __restrict__ h_in, const bf16* __restrict__ w,
                                                          bf16* __restrict__ h_out, bf16* __restrict__ x_out, int S) {
     __shared__ float red[4];
@@ -55,7 +55,7 @@ __global__ void __launch_bounds__(128) pf_rmsnorm_kernel(const int* __restrict__
 // ---- DeltaNet preparation: one CTA (128 threads) per (token, head) -----------------------------------
 // proj: [S, ldp] bf16 rows [qkv 6144 | z 2048 | b 16 | a 16].  Writes qkv_out [S, 6144] bf16 (q, k L2-normalised
 // in bf16 arithmetic, v after conv + SiLU), beta [S,16] (bf16-rounded sigmoid), g [S,16] (f32 log-decay).
-__global__ void __launch_bounds__(128) pf_dn_prep_kernel(const bf16* __restrict__ proj, int ldp, const bf16* __restrict__ conv_w,
+static __global__ void __launch_bounds__(128) pf_dn_prep_kernel(const bf16* __restrict__ proj, int ldp, const bf16* __restrict__ conv_w,
                                                          const bf16* __restrict__ a_log, const bf16* __restrict__ dt_bias,
                                                          bf16* __restrict__ qkv_out, float* __restrict__ beta, float* __restrict__ g, int S) {
     __shared__ float red[2][4];
@@ -106,7 +106,7 @@ __global__ void __launch_bounds__(128) pf_dn_prep_kernel(const bf16* __restrict_
 }
 
 // conv window after the prompt: the last four inputs per channel, zero-padded on the left, newest last
-__global__ void pf_conv_state_kernel(const bf16* __restrict__ proj, int ldp, float* __restrict__ conv, int S) {
+static __global__ void pf_conv_state_kernel(const bf16* __restrict__ proj, int ldp, float* __restrict__ conv, int S) {
     const int ch = blockIdx.x * blockDim.x + threadIdx.x;
     if (ch >= DN_CONV_CH) return;
     float4 st;
@@ -131,7 +131,7 @@ struct ChunkScratch {          // one record per (head, chunk), floats
 
 constexpr int CHUNK_LOCAL_SMEM = (2 * DN_CHUNK * (DN_K + 1) + DN_CHUNK * DN_V + DN_CHUNK * (DN_CHUNK + 1) + 3 * DN_CHUNK) * 4;
 
-__global__ void __launch_bounds__(256) pf_dn_chunk_local_kernel(const bf16* __restrict__ qkv, const float* __restrict__ beta,
+static __global__ void __launch_bounds__(256) pf_dn_chunk_local_kernel(const bf16* __restrict__ qkv, const float* __restrict__ beta,
                                                                 const float* __restrict__ g, ChunkScratch* __restrict__ scratch,
                                                                 int S, int nchunks) {
     extern __shared__ float sm[];
@@ -215,7 +215,7 @@ __global__ void __launch_bounds__(256) pf_dn_chunk_local_kernel(const bf16* __re
 constexpr int SCAN_VW = 16;
 constexpr int CHUNK_SCAN_SMEM = (3 * DN_CHUNK * (DN_K + 1) + DN_CHUNK * (DN_CHUNK + 1) + 2 * DN_CHUNK * SCAN_VW + DN_K * SCAN_VW + 2 * DN_CHUNK) * 4;
 
-__global__ void __launch_bounds__(256) pf_dn_chunk_scan_kernel(const bf16* __restrict__ qkv, const ChunkScratch* __restrict__ scratch,
+static __global__ void __launch_bounds__(256) pf_dn_chunk_scan_kernel(const bf16* __restrict__ qkv, const ChunkScratch* __restrict__ scratch,
                                                                bf16* __restrict__ core_out, float* __restrict__ state_out,
                                                                int S, int nchunks) {
     extern __shared__ float sm[];
@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(256) pf_dn_chunk_scan_kernel(const bf16* __res
 }
 
 // ---- gated RMSNorm of the DeltaNet output: one warp per (token, head) --------------------------------
-__global__ void __launch_bounds__(256) pf_gated_norm_kernel(const bf16* __restrict__ core, const bf16* __restrict__ proj, int ldp,
+static __global__ void __launch_bounds__(256) pf_gated_norm_kernel(const bf16* __restrict__ core, const bf16* __restrict__ proj, int ldp,
                                                             const bf16* __restrict__ norm_w, bf16* __restrict__ out, int S) {
     const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (gw >= S * DN_HEADS) return;
@@ -334,7 +334,7 @@ __global__ void __launch_bounds__(256) pf_gated_norm_kernel(const bf16* __restri
 // proj rows: [per head q(256) | gate(256)] x 8, k 512, v 512.  q -> q_out [S, 2048]; k, v -> cache rows [kv_head][t][256].
 struct RopeTable { float f[FA_ROT / 2]; };
 
-__global__ void __launch_bounds__(256) pf_qk_norm_rope_kernel(const bf16* __restrict__ proj, int ldp, const bf16* __restrict__ qn_w,
+static __global__ void __launch_bounds__(256) pf_qk_norm_rope_kernel(const bf16* __restrict__ proj, int ldp, const bf16* __restrict__ qn_w,
                                                               const bf16* __restrict__ kn_w, const RopeTable inv_freq,
                                                               bf16* __restrict__ q_out, bf16* __restrict__ k_cache, bf16* __restrict__ v_cache,
                                                               int S, int max_seq) {
@@ -372,7 +372,7 @@ __global__ void __launch_bounds__(256) pf_qk_norm_rope_kernel(const bf16* __rest
 constexpr int ATT_PF_MAX_S = 4096;
 constexpr int ATT_PF_WARPS = 8;
 
-__global__ void __launch_bounds__(ATT_PF_WARPS * 32) pf_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k_cache,
+static __global__ void __launch_bounds__(ATT_PF_WARPS * 32) pf_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k_cache,
                                                                          const bf16* __restrict__ v_cache, const bf16* __restrict__ proj, int ldp,
                                                                          bf16* __restrict__ out, int S, int max_seq) {
     extern __shared__ float att_sm[];
@@ -434,7 +434,7 @@ __global__ void __launch_bounds__(ATT_PF_WARPS * 32) pf_attention_kernel(const b
 }
 
 // ---- last-token LM head: GEMV over the vocabulary + arg-max (lowest index among equal bf16 maxima) -----
-__global__ void __launch_bounds__(256) pf_lm_head_kernel(const bf16* __restrict__ x, const bf16* __restrict__ lm, float* __restrict__ bmv,
+static __global__ void __launch_bounds__(256) pf_lm_head_kernel(const bf16* __restrict__ x, const bf16* __restrict__ lm, float* __restrict__ bmv,
                                                          int* __restrict__ bmi, float* __restrict__ logits_out) {
     __shared__ float sv[8];
     __shared__ int si[8];
@@ -475,7 +475,7 @@ __global__ void __launch_bounds__(256) pf_lm_head_kernel(const bf16* __restrict_
 
 // NVFP4 LM head (tensor-core layout: packed E2M1 [V,512], E4M3 block scales in 128x4 swizzled tiles), one warp per row.
 // Reference: lm_head_kernel_nvfp4 (kernel_gb10_nvfp4.cu:1451-1523), the path its hybrid prefill ends with.
-__global__ void __launch_bounds__(256) pf_lm_head_fp4_kernel(const bf16* __restrict__ x, const uint8_t* __restrict__ packed,
+static __global__ void __launch_bounds__(256) pf_lm_head_fp4_kernel(const bf16* __restrict__ x, const uint8_t* __restrict__ packed,
                                                              const uint8_t* __restrict__ scales, float* __restrict__ bmv, int* __restrict__ bmi,
                                                              float* __restrict__ logits_out) {
     __shared__ float sv[8];
@@ -521,7 +521,7 @@ __global__ void __launch_bounds__(256) pf_lm_head_fp4_kernel(const bf16* __restr
     }
 }
 
-__global__ void pf_lm_reduce_kernel(const float* __restrict__ bmv, const int* __restrict__ bmi, int n, int* __restrict__ out_token) {
+static __global__ void pf_lm_reduce_kernel(const float* __restrict__ bmv, const int* __restrict__ bmi, int n, int* __restrict__ out_token) {
     float bv = -INFINITY; int bi = 0x7fffffff;
     for (int i = threadIdx.x; i < n; i += 32) {
         const float v = bmv[i]; const int k = bmi[i];

@@ -46,6 +46,18 @@ class PrefillArgs(C.Structure):
     ]
 
 
+class BatchedArgs(C.Structure):
+    _fields_ = [
+        ("batch", C.c_int), ("max_ctx", C.c_int), ("num_pages", C.c_int), ("max_pages", C.c_int),
+        ("tokens_in", C.c_void_p), ("tokens_out", C.c_void_p), ("positions", C.c_void_p), ("block_table", C.c_void_p),
+        ("embed_weight", C.c_void_p), ("layer_weights", C.c_void_p), ("fused_layer_weights", C.c_void_p),
+        ("final_norm_weight", C.c_void_p), ("lm_head_weight", C.c_void_p),
+        ("k_pages", C.c_void_p), ("v_pages", C.c_void_p), ("dn_states", C.c_void_p), ("conv_bufs", C.c_void_p),
+        ("logits_out", C.c_void_p), ("dbg_hidden", C.c_void_p), ("dbg_teacher", C.c_void_p),
+        ("advance_positions", C.c_int), ("dbg_num_layers", C.c_int),
+    ]
+
+
 _lib = None
 
 # name -> (restype, argtypes); every symbol include/qwen35_b200.h declares
@@ -62,6 +74,7 @@ SIGNATURES = {
     "launch_prefill_bf16": (_i, [_vp, _i, _vp] + [_vp] * 5 + [_vp] * 4 + [_vp] * 3 + [_vp] * 5 + [_vp] * 5 + [_vp] * 4 + [_vp]),
     "launch_quantize_nvfp4_out": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp]),
     "launch_quantize_nvfp4_lm_out": (_i, [_vp, _i, _i, _vp, _vp, _vp]),
+    "qwen35_b200_decode_batched": (_i, [C.POINTER(BatchedArgs), _vp]),
     "qwen35_b200_gemm_bf16": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "qwen35_b200_status": (_i, [_vp]),
     "qwen35_b200_clear_status": (_i, [_vp]),

@@ -423,3 +423,90 @@ class Decoder:
                 out = out[:out.index(eos)]
             return self.tokenizer.decode(out, skip_special_tokens=True)
         return out
+
+
+KV_PAGE = 64
+
+
+class BatchedDecoder:
+    """`batch` independent sequences decoded together on one GPU (BASELINE configuration "64 sequences per GPU").
+    Each sequence owns its DeltaNet state, conv window and KV pages; weights are shared.  Prefill a sequence with
+    `prefill(seq, ids)` (runs the bs=1 batched-prefill kernels into that sequence's slots), then `step()` advances
+    every sequence by one greedy token."""
+
+    def __init__(self, weights, batch, max_ctx=2304, device="cuda"):
+        self._lib = _capi.lib()
+        self.device = torch.device(device)
+        self.batch = int(batch)
+        self.max_ctx = int(max_ctx)
+        self.max_pages = (self.max_ctx + KV_PAGE - 1) // KV_PAGE
+        self.num_pages = self.batch * self.max_pages
+        self._weights = weights
+        _attach_prefill_fused_weights(weights)
+        self._layer_weights_packed = _pack_layer_weights(weights["layer_data"], device)
+        self._prefill_fused_weights_packed = _pack_prefill_fused_layer_weights(weights["prefill_fused_layer_data"], device)
+        dev = self.device
+        self.k_pages = torch.zeros(6, self.num_pages, FA_NUM_KV_HEADS, KV_PAGE, FA_HEAD_DIM, dtype=torch.bfloat16, device=dev)
+        self.v_pages = torch.zeros_like(self.k_pages)
+        self.dn_states = torch.zeros(self.batch, 18, DN_NUM_HEADS, DN_VALUE_DIM, DN_KEY_DIM, dtype=torch.float32, device=dev)
+        self.conv_bufs = torch.zeros(self.batch, 18, DN_CONV_CHANNELS, DN_CONV_KERNEL, dtype=torch.float32, device=dev)
+        # sequence b owns pages [b*max_pages, (b+1)*max_pages): the identity table of an unfragmented pool
+        self.block_table = torch.arange(self.num_pages, dtype=torch.int32, device=dev).view(self.batch, self.max_pages).contiguous()
+        self.positions = torch.zeros(self.batch, dtype=torch.int32, device=dev)
+        self.tokens = torch.zeros(self.batch, dtype=torch.int32, device=dev)
+        self._out = torch.zeros(self.batch, dtype=torch.int32, device=dev)
+        self._one = None
+
+    def load_sequence(self, seq, k_cache, v_cache, dn_states, conv_bufs, position, next_token):
+        """Install a prefilled bs=1 state ([6,2,L,256] caches, [18,16,128,128] state, [18,6144,4] conv) as sequence `seq`."""
+        L = int(position)
+        kp = self.k_pages[:, seq * self.max_pages:(seq + 1) * self.max_pages]        # [6, pages, 2, 64, 256]
+        vp = self.v_pages[:, seq * self.max_pages:(seq + 1) * self.max_pages]
+        pad = self.max_pages * KV_PAGE
+        kk = torch.zeros(6, FA_NUM_KV_HEADS, pad, FA_HEAD_DIM, dtype=torch.bfloat16, device=self.device)
+        vv = torch.zeros_like(kk)
+        kk[:, :, :L] = k_cache[:, :, :L]
+        vv[:, :, :L] = v_cache[:, :, :L]
+        kp.copy_(kk.view(6, FA_NUM_KV_HEADS, self.max_pages, KV_PAGE, FA_HEAD_DIM).permute(0, 2, 1, 3, 4))
+        vp.copy_(vv.view(6, FA_NUM_KV_HEADS, self.max_pages, KV_PAGE, FA_HEAD_DIM).permute(0, 2, 1, 3, 4))
+        self.dn_states[seq].copy_(dn_states)
+        self.conv_bufs[seq].copy_(conv_bufs)
+        self.positions[seq] = L
+        self.tokens[seq] = int(next_token)
+
+    def prefill(self, seq, token_ids):
+        """Prefill one sequence with the bs=1 prefill path and install it."""
+        if self._one is None:
+            self._one = Decoder(weights=self._weights, max_seq_len=self.max_pages * KV_PAGE, device=self.device)
+        first = self._one.prefill_tokens(token_ids)
+        self.load_sequence(seq, self._one._fa_k_cache, self._one._fa_v_cache, self._one._dn_states, self._one._conv_bufs,
+                           int(token_ids.numel()), first)
+        return first
+
+    def _args(self, **kw):
+        a = _capi.BatchedArgs()
+        a.batch = self.batch; a.max_ctx = self.max_ctx; a.num_pages = self.num_pages; a.max_pages = self.max_pages
+        a.tokens_in = self.tokens.data_ptr(); a.tokens_out = self._out.data_ptr(); a.positions = self.positions.data_ptr()
+        a.block_table = self.block_table.data_ptr()
+        a.embed_weight = self._weights["embed_weight"].data_ptr(); a.layer_weights = self._layer_weights_packed.data_ptr()
+        a.fused_layer_weights = self._prefill_fused_weights_packed.data_ptr()
+        a.final_norm_weight = self._weights["final_norm_weight"].data_ptr(); a.lm_head_weight = self._weights["lm_head_weight"].data_ptr()
+        a.k_pages = self.k_pages.data_ptr(); a.v_pages = self.v_pages.data_ptr()
+        a.dn_states = self.dn_states.data_ptr(); a.conv_bufs = self.conv_bufs.data_ptr()
+        a.advance_positions = 1
+        for k, v in kw.items():
+            setattr(a, k, v)
+        return a
+
+    def step(self, **kw):
+        """One greedy token for every sequence; the new tokens become the next step's inputs.  Returns int32 [batch] (GPU)."""
+        a = self._args(**{k: (_capi.ptr(v) if torch.is_tensor(v) else v) for k, v in kw.items()})
+        with torch.cuda.device(self.device):
+            _capi.check(self._lib.qwen35_b200_decode_batched(C.byref(a), C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)),
+                        "decode_batched")
+        self.tokens, self._out = self._out, self.tokens
+        return self.tokens
+
+    def check_status(self):
+        with torch.cuda.device(self.device):
+            _capi.check(self._lib.qwen35_b200_status(C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)), "device status")
