@@ -197,7 +197,10 @@ int launch_quantize_nvfp4_lm_out(const void* weight, int rows, int cols, void* p
  *   k_pages / v_pages       bf16 [6][num_pages][2][64][256], addressed through block_table int32 [batch][max_pages]
  *   dn_states f32 [batch][18][16][128][128]          conv_bufs f32 [batch][18][6144][4]
  * max_ctx bounds positions+1 (<= 8192).  advance_positions != 0 increments positions[] on the device after the
- * step, so steps chain without host work.  Weights are the bf16 tables of launch_prefill_bf16. */
+ * step, so steps chain without host work.  Weights are the bf16 tables of launch_prefill_bf16.
+ * layer_weights_host / fused_layer_weights_host: optional host copies of the two device tables (same bytes).  With
+ * them the call never synchronises, so steps can be queued back to back; without them it reads the device tables
+ * back on every call (a stream synchronisation per step). */
 typedef struct {
     int batch; int max_ctx; int num_pages; int max_pages;
     const int* tokens_in; int* tokens_out; int* positions; const int* block_table;
@@ -209,6 +212,7 @@ typedef struct {
     const void* dbg_teacher;   /* optional bf16 [24][batch][1024]: layer l>0 reads row block l as its input */
     int advance_positions;
     int dbg_num_layers;
+    const void* layer_weights_host; const void* fused_layer_weights_host;
 } Qwen35BatchedArgs;
 int qwen35_b200_decode_batched(const Qwen35BatchedArgs* args, qwen35_stream_t stream);
 

@@ -142,54 +142,134 @@ __global__ void __launch_bounds__(256) bd_qk_norm_rope_kernel(const bf16* __rest
     for (int i = 0; i < 8; ++i) dst[lane + 32 * i] = f2bf(xv[i]);
 }
 
-// ---- decode attention over the paged cache: one warp per (sequence, q head), exact bf16 rounding points ----
-constexpr int BD_ATT_WARPS = 4;
-__global__ void __launch_bounds__(BD_ATT_WARPS * 32) bd_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k_pages,
-                                                                         const bf16* __restrict__ v_pages, const int* __restrict__ positions,
-                                                                         const int* __restrict__ table, int max_pages, const bf16* __restrict__ proj,
-                                                                         int ldp, bf16* __restrict__ out, int B, int max_ctx) {
-    extern __shared__ float bd_sm[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int gw = blockIdx.x * BD_ATT_WARPS + warp;
-    if (gw >= B * FA_Q_HEADS) return;
-    const int b = gw / FA_Q_HEADS, head = gw % FA_Q_HEADS, kvh = head / FA_GQA;
-    float* sc = bd_sm + (size_t)warp * max_ctx;
-    float* sqv = bd_sm + (size_t)BD_ATT_WARPS * max_ctx + warp * FA_HEAD_DIM;
-    const int L = positions[b] + 1;
-    for (int i = lane; i < FA_HEAD_DIM; i += 32) sqv[i] = bf2f(q[(size_t)b * FA_Q_SIZE + head * FA_HEAD_DIM + i]);
-    __syncwarp();
+// ---- decode attention over the paged cache, split over the context -----------------------------------------
+// Three kernels per layer keep the bf16 rounding points of the bs=1 path (P is rounded with the global normaliser):
+//   scores  one CTA per (sequence, kv head, chunk of 128 positions): bf16(q.k)/16 for the four q heads of the kv
+//           head (K row read once, coalesced), chunk max and sum-exp per head
+//   pv      same grid: global max / normaliser from the chunk statistics, P = bf16(exp(s-m)/l), partial P.V
+//   merge   one warp per (sequence, q head): sum of the partials in chunk order, bf16, times bf16(sigmoid(gate))
+constexpr int BD_CHUNK = 128;
+
+__device__ __forceinline__ const bf16* kv_row_c(const bf16* pages, const int* tb, int kvh, int pos) {
+    return pages + (((size_t)tb[pos / KV_PAGE] * FA_KV_HEADS + kvh) * KV_PAGE + (pos % KV_PAGE)) * FA_HEAD_DIM;
+}
+
+__global__ void __launch_bounds__(128) bd_att_scores_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k_pages,
+                                                            const int* __restrict__ positions, const int* __restrict__ table, int max_pages,
+                                                            float* __restrict__ scores, float* __restrict__ stats, int max_ctx, int max_chunks) {
+    __shared__ float ssc[FA_GQA][BD_CHUNK];
+    const int b = blockIdx.x, kvh = blockIdx.y, c = blockIdx.z, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int L = positions[b] + 1, j0 = c * BD_CHUNK;
+    if (j0 >= L) return;
+    const int j1 = min(L, j0 + BD_CHUNK);
     const int* tb = table + b * max_pages;
-    float mx = -INFINITY;
-    for (int j = lane; j < L; j += 32) {
-        const uint4* kr = reinterpret_cast<const uint4*>(k_pages + (((size_t)tb[j / KV_PAGE] * FA_KV_HEADS + kvh) * KV_PAGE + (j % KV_PAGE)) * FA_HEAD_DIM);
-        float d = 0.f;
-#pragma unroll 4
-        for (int c = 0; c < FA_HEAD_DIM / 8; ++c) {
-            const uint4 kv = kr[c];
-            const float* qq = sqv + c * 8;
-            d = fmaf(qq[0], bf_lo(kv.x), d); d = fmaf(qq[1], bf_hi(kv.x), d);
-            d = fmaf(qq[2], bf_lo(kv.y), d); d = fmaf(qq[3], bf_hi(kv.y), d);
-            d = fmaf(qq[4], bf_lo(kv.z), d); d = fmaf(qq[5], bf_hi(kv.z), d);
-            d = fmaf(qq[6], bf_lo(kv.w), d); d = fmaf(qq[7], bf_hi(kv.w), d);
-        }
-        const float s = rbf(d) * 0.0625f;
-        sc[j] = s;
-        mx = fmaxf(mx, s);
+    float qr[FA_GQA][8];
+#pragma unroll
+    for (int g = 0; g < FA_GQA; ++g) {
+        const uint4 qv = *(reinterpret_cast<const uint4*>(q + (size_t)b * FA_Q_SIZE + (kvh * FA_GQA + g) * FA_HEAD_DIM) + lane);
+        qr[g][0] = bf_lo(qv.x); qr[g][1] = bf_hi(qv.x); qr[g][2] = bf_lo(qv.y); qr[g][3] = bf_hi(qv.y);
+        qr[g][4] = bf_lo(qv.z); qr[g][5] = bf_hi(qv.z); qr[g][6] = bf_lo(qv.w); qr[g][7] = bf_hi(qv.w);
     }
-    mx = warp_max(mx);
-    float sm = 0.f;
-    for (int j = lane; j < L; j += 32) sm += expf(sc[j] - mx);
-    sm = warp_sum(sm);
-    for (int j = lane; j < L; j += 32) sc[j] = rbf(expf(sc[j] - mx) / sm);
-    __syncwarp();
+    for (int j = j0 + warp; j < j1; j += 8) {          // two positions in flight per warp
+        const int jb = j + 4;
+        const uint4 ka = *(reinterpret_cast<const uint4*>(kv_row_c(k_pages, tb, kvh, j)) + lane);
+        const uint4 kb = (jb < j1) ? *(reinterpret_cast<const uint4*>(kv_row_c(k_pages, tb, kvh, jb)) + lane) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const int jj = r ? jb : j;
+            if (jj >= j1) break;
+            const uint4 kv = r ? kb : ka;
+            const float kf[8] = {bf_lo(kv.x), bf_hi(kv.x), bf_lo(kv.y), bf_hi(kv.y), bf_lo(kv.z), bf_hi(kv.z), bf_lo(kv.w), bf_hi(kv.w)};
+#pragma unroll
+            for (int g = 0; g < FA_GQA; ++g) {
+                float d = 0.f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) d = fmaf(qr[g][i], kf[i], d);
+                d = warp_sum(d);
+                if (lane == 0) ssc[g][jj - j0] = rbf(d) * 0.0625f;
+            }
+        }
+    }
+    __syncthreads();
+    const int cn = j1 - j0;
+    {   // warp g: statistics of head g over this chunk; all threads: scores to global
+        const int g = warp;
+        float mx = -INFINITY;
+        for (int j = lane; j < cn; j += 32) mx = fmaxf(mx, ssc[g][j]);
+        mx = warp_max(mx);
+        float sm = 0.f;
+        for (int j = lane; j < cn; j += 32) sm += expf(ssc[g][j] - mx);
+        sm = warp_sum(sm);
+        const int head = kvh * FA_GQA + g;
+        if (lane == 0) {
+            float* st = stats + (((size_t)b * FA_Q_HEADS + head) * max_chunks + c) * 2;
+            st[0] = mx; st[1] = sm;
+        }
+        float* dst = scores + ((size_t)b * FA_Q_HEADS + head) * max_ctx + j0;
+        for (int j = lane; j < cn; j += 32) dst[j] = ssc[g][j];
+    }
+}
+
+__global__ void __launch_bounds__(128) bd_att_pv_kernel(const bf16* __restrict__ v_pages, const int* __restrict__ positions,
+                                                        const int* __restrict__ table, int max_pages, const float* __restrict__ scores,
+                                                        const float* __restrict__ stats, float* __restrict__ partial, int max_ctx, int max_chunks) {
+    __shared__ float sp[FA_GQA][BD_CHUNK];
+    __shared__ float sml[FA_GQA][2];
+    const int b = blockIdx.x, kvh = blockIdx.y, c = blockIdx.z, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int L = positions[b] + 1, j0 = c * BD_CHUNK;
+    if (j0 >= L) return;
+    const int j1 = min(L, j0 + BD_CHUNK), cn = j1 - j0;
+    const int nch = (L + BD_CHUNK - 1) / BD_CHUNK;
+    const int* tb = table + b * max_pages;
+    {
+        const int head = kvh * FA_GQA + warp;
+        const float* st = stats + ((size_t)b * FA_Q_HEADS + head) * max_chunks * 2;
+        float mx = -INFINITY;
+        for (int k = lane; k < nch; k += 32) mx = fmaxf(mx, st[2 * k]);
+        mx = warp_max(mx);
+        float sm = 0.f;
+        for (int k = lane; k < nch; k += 32) sm += st[2 * k + 1] * expf(st[2 * k] - mx);
+        sm = warp_sum(sm);
+        if (lane == 0) { sml[warp][0] = mx; sml[warp][1] = sm; }
+    }
+    __syncthreads();
+    for (int i = tid; i < FA_GQA * cn; i += 128) {
+        const int g = i / cn, j = i % cn;
+        sp[g][j] = rbf(expf(scores[((size_t)b * FA_Q_HEADS + kvh * FA_GQA + g) * max_ctx + j0 + j] - sml[g][0]) / sml[g][1]);
+    }
+    __syncthreads();
+    float acc[FA_GQA][2];
+#pragma unroll
+    for (int g = 0; g < FA_GQA; ++g) { acc[g][0] = 0.f; acc[g][1] = 0.f; }
+    for (int j = 0; j < cn; j += 4) {
+        uint32_t vr[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) vr[u] = (j + u < cn) ? *(reinterpret_cast<const uint32_t*>(kv_row_c(v_pages, tb, kvh, j0 + j + u)) + tid) : 0u;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (j + u < cn) {
+                const float v0 = bf_lo(vr[u]), v1 = bf_hi(vr[u]);
+#pragma unroll
+                for (int g = 0; g < FA_GQA; ++g) { const float p = sp[g][j + u]; acc[g][0] = fmaf(p, v0, acc[g][0]); acc[g][1] = fmaf(p, v1, acc[g][1]); }
+            }
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < FA_GQA; ++g)
+        reinterpret_cast<float2*>(partial + (((size_t)b * FA_Q_HEADS + kvh * FA_GQA + g) * max_chunks + c) * FA_HEAD_DIM)[tid] = make_float2(acc[g][0], acc[g][1]);
+}
+
+__global__ void __launch_bounds__(256) bd_att_merge_kernel(const float* __restrict__ partial, const int* __restrict__ positions,
+                                                           const bf16* __restrict__ proj, int ldp, bf16* __restrict__ out, int B, int max_chunks) {
+    const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (gw >= B * FA_Q_HEADS) return;
+    const int b = gw / FA_Q_HEADS, head = gw % FA_Q_HEADS;
+    const int nch = (positions[b] + 1 + BD_CHUNK - 1) / BD_CHUNK;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < L; ++j) {
-        const float p = sc[j];
-        const uint4 vv = *(reinterpret_cast<const uint4*>(v_pages + (((size_t)tb[j / KV_PAGE] * FA_KV_HEADS + kvh) * KV_PAGE + (j % KV_PAGE)) * FA_HEAD_DIM) + lane);
-        acc[0] = fmaf(p, bf_lo(vv.x), acc[0]); acc[1] = fmaf(p, bf_hi(vv.x), acc[1]);
-        acc[2] = fmaf(p, bf_lo(vv.y), acc[2]); acc[3] = fmaf(p, bf_hi(vv.y), acc[3]);
-        acc[4] = fmaf(p, bf_lo(vv.z), acc[4]); acc[5] = fmaf(p, bf_hi(vv.z), acc[5]);
-        acc[6] = fmaf(p, bf_lo(vv.w), acc[6]); acc[7] = fmaf(p, bf_hi(vv.w), acc[7]);
+    const float* pb = partial + ((size_t)b * FA_Q_HEADS + head) * max_chunks * FA_HEAD_DIM + lane * 8;
+    for (int c = 0; c < nch; ++c) {
+        const float4 a0 = *reinterpret_cast<const float4*>(pb + (size_t)c * FA_HEAD_DIM), a1 = *reinterpret_cast<const float4*>(pb + (size_t)c * FA_HEAD_DIM + 4);
+        acc[0] += a0.x; acc[1] += a0.y; acc[2] += a0.z; acc[3] += a0.w; acc[4] += a1.x; acc[5] += a1.y; acc[6] += a1.z; acc[7] += a1.w;
     }
     const uint4 gr = *(reinterpret_cast<const uint4*>(proj + (size_t)b * ldp + head * 2 * FA_HEAD_DIM + FA_HEAD_DIM) + lane);
     const float gv[8] = {bf_lo(gr.x), bf_hi(gr.x), bf_lo(gr.y), bf_hi(gr.y), bf_lo(gr.z), bf_hi(gr.z), bf_lo(gr.w), bf_hi(gr.w)};
@@ -259,25 +339,7 @@ static void* batched_scratch(size_t bytes) {
 }
 
 struct PrefillFusedB { const void* proj_weight; const void* gate_up_weight; const void* unused[4]; };
-struct HostTablesB { const void* dev_layers; const void* dev_fused; LayerRec layers[NUM_LAYERS]; PrefillFusedB fused[NUM_LAYERS]; };
-static HostTablesB g_btables[8];
-static int g_btables_n = 0;
-static std::mutex g_btables_mu;
-
-static const HostTablesB* host_tables_b(const void* dev_layers, const void* dev_fused) {
-    std::lock_guard<std::mutex> lk(g_btables_mu);
-    for (int i = 0; i < g_btables_n; ++i)
-        if (g_btables[i].dev_layers == dev_layers && g_btables[i].dev_fused == dev_fused) return &g_btables[i];
-    HostTablesB* t = &g_btables[g_btables_n < 8 ? g_btables_n++ : 7];
-    t->dev_layers = dev_layers; t->dev_fused = dev_fused;
-    if (cudaMemcpy(t->layers, dev_layers, sizeof(t->layers), cudaMemcpyDeviceToHost) != cudaSuccess ||
-        cudaMemcpy(t->fused, dev_fused, sizeof(t->fused), cudaMemcpyDeviceToHost) != cudaSuccess) {
-        set_error("reading the layer tables failed");
-        t->dev_layers = nullptr;
-        return nullptr;
-    }
-    return t;
-}
+struct HostTablesB { LayerRec layers[NUM_LAYERS]; PrefillFusedB fused[NUM_LAYERS]; };
 
 }  // namespace q35
 
@@ -301,17 +363,28 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
         set_error("null tensor pointer");
         return QWEN35_ERR_BAD_ARG;
     }
-    const HostTablesB* t = host_tables_b(in->layer_weights, in->fused_layer_weights);
-    if (!t) return QWEN35_ERR_CUDA;
-    static bool attr_done = false;
-    if (!attr_done) {
-        Q35_CUDA_OK(cudaFuncSetAttribute(bd_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)((BD_ATT_WARPS * 8192 + BD_ATT_WARPS * FA_HEAD_DIM) * sizeof(float))));
-        attr_done = true;
+    // Layer tables on the host: the caller's host copies when given (no synchronisation: steps can be queued
+    // back to back), else read back from the device tables on every call (never cached: a re-packed table can
+    // come back at the same device address).
+    HostTablesB tables;
+    const LayerRec* layers_h = reinterpret_cast<const LayerRec*>(in->layer_weights_host);
+    const PrefillFusedB* fused_h = reinterpret_cast<const PrefillFusedB*>(in->fused_layer_weights_host);
+    if (!layers_h || !fused_h) {
+        if (cudaMemcpyAsync(tables.layers, in->layer_weights, sizeof(tables.layers), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+            cudaMemcpyAsync(tables.fused, in->fused_layer_weights, sizeof(tables.fused), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+            cudaStreamSynchronize(stream) != cudaSuccess) {
+            set_error("reading the layer tables failed: %s", cudaGetErrorString(cudaGetLastError()));
+            return QWEN35_ERR_CUDA;
+        }
+        layers_h = tables.layers; fused_h = tables.fused;
     }
     // scratch rows of B tokens
     const size_t rows = (size_t)B;
     const size_t n_hidden = rows * HIDDEN, n_proj = rows * DN_PROJ_ROWS, n_att = rows * 2048, n_mlp = rows * INTER, n_logits = rows * VOCAB;
-    const size_t total = (3 * n_hidden + n_proj + 3 * n_att + n_mlp + n_logits) * sizeof(bf16) + 4096;
+    const int max_chunks = (in->max_ctx + BD_CHUNK - 1) / BD_CHUNK;
+    const size_t n_scores = rows * FA_Q_HEADS * (size_t)in->max_ctx, n_stats = rows * FA_Q_HEADS * max_chunks * 2,
+                 n_part = rows * FA_Q_HEADS * max_chunks * FA_HEAD_DIM;
+    const size_t total = (3 * n_hidden + n_proj + 3 * n_att + n_mlp + n_logits) * sizeof(bf16) + (n_scores + n_stats + n_part) * sizeof(float) + 4096;
     char* base = (char*)batched_scratch(total);
     if (!base) return QWEN35_ERR_CUDA;
     bf16* hidden = (bf16*)base;
@@ -323,6 +396,9 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
     bf16* attn = core + n_att;
     bf16* mlp = attn + n_att;
     bf16* logits = mlp + n_mlp;
+    float* att_scores = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(logits + n_logits) + 255) & ~(uintptr_t)255);
+    float* att_stats = att_scores + n_scores;
+    float* att_part = att_stats + n_stats;
     RopeTable rt;
     for (int i = 0; i < FA_ROT / 2; ++i) rt.f[i] = 1.0f / (float)std::pow(1.0e7, (double)((float)(2 * i) / (float)FA_ROT));
     const size_t conv_stride = (size_t)N_DN * DN_CONV_CH * 4, state_stride = (size_t)N_DN * DN_HEADS * DN_V * DN_K;
@@ -331,8 +407,8 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
 
     int i_dn = 0, i_fa = 0;
     for (int layer = 0; layer < n_layers; ++layer) {
-        const LayerRec& L = t->layers[layer];
-        const PrefillFusedB& F = t->fused[layer];
+        const LayerRec& L = layers_h[layer];
+        const PrefillFusedB& F = fused_h[layer];
         if (layer > 0 && in->dbg_teacher)
             bd_copy_rows_kernel<<<(int)((n_hidden / 8 + 255) / 256), 256, 0, stream>>>((const bf16*)in->dbg_teacher + (size_t)layer * n_hidden, hidden, (int)(n_hidden / 8));
         pf_rmsnorm_kernel<<<B, 128, 0, stream>>>(layer == 0 ? in->tokens_in : nullptr, (const bf16*)in->embed_weight, hidden, (const bf16*)L.p[0],
@@ -357,10 +433,11 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
             bf16* vp = (bf16*)in->v_pages + (size_t)i_fa * page_layer_stride;
             bd_qk_norm_rope_kernel<<<(B * 12 + 7) / 8, 256, 0, stream>>>(proj, ldp, (const bf16*)L.p[FA_QNORM], (const bf16*)L.p[FA_KNORM], rt,
                                                                          in->positions, in->block_table, in->max_pages, qbuf, kp, vp, B);
-            const size_t smem = ((size_t)BD_ATT_WARPS * in->max_ctx + BD_ATT_WARPS * FA_HEAD_DIM) * sizeof(float);
-            bd_attention_kernel<<<(B * FA_Q_HEADS + BD_ATT_WARPS - 1) / BD_ATT_WARPS, BD_ATT_WARPS * 32, smem, stream>>>(
-                qbuf, kp, vp, in->positions, in->block_table, in->max_pages, proj, ldp, attn, B, in->max_ctx);
-            g_launches.fetch_add(2);
+            const dim3 agrid(B, FA_KV_HEADS, max_chunks);
+            bd_att_scores_kernel<<<agrid, 128, 0, stream>>>(qbuf, kp, in->positions, in->block_table, in->max_pages, att_scores, att_stats, in->max_ctx, max_chunks);
+            bd_att_pv_kernel<<<agrid, 128, 0, stream>>>(vp, in->positions, in->block_table, in->max_pages, att_scores, att_stats, att_part, in->max_ctx, max_chunks);
+            bd_att_merge_kernel<<<(B * FA_Q_HEADS + 7) / 8, 256, 0, stream>>>(att_part, in->positions, proj, ldp, attn, B, max_chunks);
+            g_launches.fetch_add(4);
             w_out = (const bf16*)L.p[FA_O]; w_post = (const bf16*)L.p[FA_POST_NORM]; w_down = (const bf16*)L.p[FA_DOWN];
             ++i_fa;
         }

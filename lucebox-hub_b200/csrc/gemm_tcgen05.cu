@@ -2,9 +2,10 @@
 // projections:  C[M,N] = A[M,K] . B[N,K]^T  with f32 accumulation in tensor memory.
 //
 // Replaces the cuBLAS calls of the reference's prefill (cublas_bf16_gemm, prefill.cu:895-903 and its
-// ten call sites :1267-1434).  One CTA computes one 128 x 128 output tile:
-//   warp 0     TMA producer: 128B-swizzled 64-wide K slices of A and B into a 6-stage ring
-//   warp 1     allocates 128 TMEM columns, then one thread issues tcgen05.mma (M128 N128 K16 x4 per
+// ten call sites :1267-1434).  One CTA computes one 128 x BN output tile (BN = 128, 64, 32 or 16: the narrow
+// tiles spread a skinny problem, M <= 128 rows of activations against a tall weight matrix, over all SMs):
+//   warp 0     TMA producer: 128B-swizzled 64-wide K slices of A and B into a ring of stages
+//   warp 1     allocates the TMEM columns, then one thread issues tcgen05.mma (M128 N=BN K16 x4 per
 //              stage) and commits each stage back to the producer
 //   warps 2-5  epilogue: tcgen05.ld the accumulator rows, round once to bf16 (what a bf16 linear
 //              layer returns), optionally fuse the residual add or silu(gate)*up, store
@@ -16,10 +17,11 @@
 
 namespace q35 {
 
-constexpr int GEMM_BM = 128, GEMM_BN = 128, GEMM_BK = 64, GEMM_STAGES = 6;
+constexpr int GEMM_BM = 128, GEMM_BK = 64;
 constexpr int GEMM_THREADS = 192;
-constexpr uint32_t GEMM_STAGE_BYTES = (GEMM_BM + GEMM_BN) * GEMM_BK * 2;   // 32 KB
-constexpr uint32_t GEMM_SMEM = GEMM_STAGES * GEMM_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+__host__ __device__ constexpr int gemm_stages(int bn) { return bn == 128 ? 6 : 4; }          // narrow tiles: two CTAs per SM
+__host__ __device__ constexpr uint32_t gemm_stage_bytes(int bn) { return (uint32_t)(GEMM_BM + bn) * GEMM_BK * 2; }
+__host__ __device__ constexpr uint32_t gemm_smem(int bn) { return gemm_stages(bn) * gemm_stage_bytes(bn) + 1024 /*align*/ + 256 /*barriers*/; }
 constexpr unsigned GEMM_SPIN_LIMIT = 20u * 1000u * 1000u;
 
 enum GemmEpi { EPI_BF16 = 0, EPI_RESIDUAL = 1, EPI_SILU_MUL = 2 };
@@ -75,7 +77,7 @@ __device__ __forceinline__ uint64_t make_smem_desc(uint32_t smem_addr) {
     return d;
 }
 // instruction descriptor: D f32, A/B bf16, both K-major, N at [17,23) in units of 8, M at [24,29) in units of 16
-constexpr uint32_t GEMM_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(GEMM_BN >> 3) << 17) | ((uint32_t)(GEMM_BM >> 4) << 24);
+__host__ __device__ constexpr uint32_t gemm_idesc(int bn) { return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(GEMM_BM >> 4) << 24); }
 
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
     asm volatile(
@@ -98,9 +100,34 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         : "r"(taddr) : "memory");
 }
 
-template <int EPI>
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr) : "memory");
+}
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+        : "r"(taddr) : "memory");
+}
+// W accumulator columns of this thread's TMEM lane, W = 8, 16 or 32
+template <int W>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[32]) {
+    if (W == 32) tmem_ld32(taddr, r);
+    else if (W == 16) tmem_ld16(taddr, r);
+    else tmem_ld8(taddr, r);
+}
+
+template <int EPI, int GEMM_BN>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
 gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+    constexpr int GEMM_STAGES = gemm_stages(GEMM_BN);
+    constexpr uint32_t GEMM_STAGE_BYTES = gemm_stage_bytes(GEMM_BN), GEMM_IDESC = gemm_idesc(GEMM_BN);
+    constexpr uint32_t TMEM_COLS = GEMM_BN < 32 ? 32u : (uint32_t)GEMM_BN;
+    constexpr int HALF = GEMM_BN / 2;          // B rows per TMA box
     extern __shared__ unsigned char g_smem_raw[];
     // 128B-swizzled tiles need 1024-byte alignment
     const uint32_t raw = g_smem_u32(g_smem_raw);
@@ -123,7 +150,7 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(g_smem_u32(tmem_slot)), "r"(128u) : "memory");
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(g_smem_u32(tmem_slot)), "r"(TMEM_COLS) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -140,13 +167,8 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
                 const uint32_t a_dst = tiles + st * GEMM_STAGE_BYTES, b_dst = a_dst + GEMM_BM * GEMM_BK * 2;
                 g_mbar_expect_tx(full0 + 8 * st, GEMM_STAGE_BYTES);
                 g_tma_load_2d(a_dst, &tmA, kb * GEMM_BK, m0, full0 + 8 * st);
-                if (EPI == EPI_SILU_MUL) {
-                    g_tma_load_2d(b_dst, &tmB, kb * GEMM_BK, n0, full0 + 8 * st);
-                    g_tma_load_2d(b_dst + 64 * GEMM_BK * 2, &tmB, kb * GEMM_BK, p.up_row_offset + n0, full0 + 8 * st);
-                } else {
-                    g_tma_load_2d(b_dst, &tmB, kb * GEMM_BK, n0, full0 + 8 * st);
-                    g_tma_load_2d(b_dst + 64 * GEMM_BK * 2, &tmB, kb * GEMM_BK, n0 + 64, full0 + 8 * st);
-                }
+                g_tma_load_2d(b_dst, &tmB, kb * GEMM_BK, n0, full0 + 8 * st);
+                g_tma_load_2d(b_dst + HALF * GEMM_BK * 2, &tmB, kb * GEMM_BK, (EPI == EPI_SILU_MUL ? p.up_row_offset : HALF) + n0, full0 + 8 * st);
                 issued = kb + 1;
             }
             // every copy this CTA issued must have landed before it may exit (matters only after an abort)
@@ -182,17 +204,18 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (ok) {
             if (EPI == EPI_SILU_MUL) {
+                constexpr int CW = HALF < 32 ? HALF : 32;      // gate columns [0, HALF), up columns [HALF, BN)
 #pragma unroll
-                for (int c = 0; c < 2; ++c) {
+                for (int c = 0; c < HALF / CW; ++c) {
                     uint32_t g[32], u[32];
-                    tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), g);
-                    tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(64 + c * 32), u);
+                    tmem_ld<CW>(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * CW), g);
+                    tmem_ld<CW>(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(HALF + c * CW), u);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                     if (row < p.M) {
-                        bf16* dst = p.C + (size_t)row * p.ldc + n0 + c * 32;
+                        bf16* dst = p.C + (size_t)row * p.ldc + n0 + c * CW;
 #pragma unroll
-                        for (int j = 0; j < 32; j += 2) {
-                            const int n = n0 + c * 32 + j;
+                        for (int j = 0; j < CW; j += 2) {
+                            const int n = n0 + c * CW + j;
                             const float m0v = rbf(silu_f(rbf(__uint_as_float(g[j])))) * rbf(__uint_as_float(u[j]));
                             const float m1v = rbf(silu_f(rbf(__uint_as_float(g[j + 1])))) * rbf(__uint_as_float(u[j + 1]));
                             if (n + 1 < p.N) *reinterpret_cast<__nv_bfloat162*>(dst + j) = __halves2bfloat162(f2bf(m0v), f2bf(m1v));
@@ -201,17 +224,18 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
                     }
                 }
             } else {
+                constexpr int CW = GEMM_BN < 32 ? GEMM_BN : 32;
 #pragma unroll
-                for (int c = 0; c < GEMM_BN / 32; ++c) {
+                for (int c = 0; c < GEMM_BN / CW; ++c) {
                     uint32_t v[32];
-                    tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
+                    tmem_ld<CW>(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * CW), v);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                     if (row < p.M) {
-                        bf16* dst = p.C + (size_t)row * p.ldc + n0 + c * 32;
-                        const bf16* res = (EPI == EPI_RESIDUAL) ? p.R + (size_t)row * p.ldr + n0 + c * 32 : nullptr;
+                        bf16* dst = p.C + (size_t)row * p.ldc + n0 + c * CW;
+                        const bf16* res = (EPI == EPI_RESIDUAL) ? p.R + (size_t)row * p.ldr + n0 + c * CW : nullptr;
 #pragma unroll
-                        for (int j = 0; j < 32; j += 2) {
-                            const int n = n0 + c * 32 + j;
+                        for (int j = 0; j < CW; j += 2) {
+                            const int n = n0 + c * CW + j;
                             float y0 = rbf(__uint_as_float(v[j])), y1 = rbf(__uint_as_float(v[j + 1]));
                             if (EPI == EPI_RESIDUAL) {
                                 if (n < p.N) y0 += bf2f(res[j]);
@@ -229,7 +253,7 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
     __syncthreads();
     if (warp == 1) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(128u) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
     }
 }
 
@@ -273,27 +297,39 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
     }
     void* ws = get_workspace();
     if (!ws) return QWEN35_ERR_CUDA;
+    if (epi < 0 || epi > 2) { set_error("gemm_bf16: unknown epilogue %d", epi); return QWEN35_ERR_BAD_ARG; }
+    // tile width: 128 unless the problem is a single row of tiles, then the widest tile that still fills the SMs
+    const int m_tiles = (M + GEMM_BM - 1) / GEMM_BM;
+    int bn = 128;
+    if (m_tiles == 1) {
+        const int want = 120;
+        while (bn > 16 && (N + (epi == EPI_SILU_MUL ? bn / 2 : bn) - 1) / (epi == EPI_SILU_MUL ? bn / 2 : bn) < want) bn >>= 1;
+    }
     CUtensorMap tmA, tmB;
-    if (!make_tmap(&tmA, A, M, K, lda, GEMM_BM) || !make_tmap(&tmB, B, b_rows, K, K, 64)) {
-        set_error("cuTensorMapEncodeTiled failed");
+    if (!make_tmap(&tmA, A, M, K, lda, GEMM_BM) || !make_tmap(&tmB, B, b_rows, K, K, bn / 2)) {
+        set_error("cuTensorMapEncodeTiled failed (A %p [%d x %d] ld %d; B %p [%d x %d] box rows %d)", (const void*)A, M, K, lda, (const void*)B, b_rows, K, bn / 2);
         return QWEN35_ERR_CUDA;
     }
     GemmParams p{M, N, K, C, ldc, R, ldr, up_row_offset, (int*)ws};
-    static bool attr_done = false;
-    if (!attr_done) {
-        Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<EPI_BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM));
-        Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<EPI_RESIDUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM));
-        Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<EPI_SILU_MUL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GEMM_SMEM));
-        attr_done = true;
+    const int bn_out = (epi == EPI_SILU_MUL) ? bn / 2 : bn;
+    dim3 grid((N + bn_out - 1) / bn_out, m_tiles);
+#define Q35_GEMM_CASE(E, BN)                                                                                                          \
+    case (E) * 1000 + (BN): {                                                                                                         \
+        static bool attr = false;                                                                                                     \
+        if (!attr) {                                                                                                                  \
+            Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<E, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem(BN))); \
+            attr = true;                                                                                                              \
+        }                                                                                                                             \
+        gemm_bf16_tcgen05_kernel<E, BN><<<grid, GEMM_THREADS, gemm_smem(BN), stream>>>(tmA, tmB, p);                                   \
+        break;                                                                                                                        \
     }
-    const int bn_out = (epi == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
-    dim3 grid((N + bn_out - 1) / bn_out, (M + GEMM_BM - 1) / GEMM_BM);
-    switch (epi) {
-        case EPI_BF16: gemm_bf16_tcgen05_kernel<EPI_BF16><<<grid, GEMM_THREADS, GEMM_SMEM, stream>>>(tmA, tmB, p); break;
-        case EPI_RESIDUAL: gemm_bf16_tcgen05_kernel<EPI_RESIDUAL><<<grid, GEMM_THREADS, GEMM_SMEM, stream>>>(tmA, tmB, p); break;
-        case EPI_SILU_MUL: gemm_bf16_tcgen05_kernel<EPI_SILU_MUL><<<grid, GEMM_THREADS, GEMM_SMEM, stream>>>(tmA, tmB, p); break;
-        default: set_error("gemm_bf16: unknown epilogue %d", epi); return QWEN35_ERR_BAD_ARG;
+    switch (epi * 1000 + bn) {
+        Q35_GEMM_CASE(EPI_BF16, 128) Q35_GEMM_CASE(EPI_BF16, 64) Q35_GEMM_CASE(EPI_BF16, 32) Q35_GEMM_CASE(EPI_BF16, 16)
+        Q35_GEMM_CASE(EPI_RESIDUAL, 128) Q35_GEMM_CASE(EPI_RESIDUAL, 64) Q35_GEMM_CASE(EPI_RESIDUAL, 32) Q35_GEMM_CASE(EPI_RESIDUAL, 16)
+        Q35_GEMM_CASE(EPI_SILU_MUL, 128) Q35_GEMM_CASE(EPI_SILU_MUL, 64) Q35_GEMM_CASE(EPI_SILU_MUL, 32) Q35_GEMM_CASE(EPI_SILU_MUL, 16)
+        default: set_error("gemm_bf16: no kernel for epilogue %d, tile %d", epi, bn); return QWEN35_ERR_BAD_ARG;
     }
+#undef Q35_GEMM_CASE
     Q35_CUDA_OK(cudaGetLastError());
     g_launches.fetch_add(1);
     return QWEN35_OK;

@@ -138,26 +138,20 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
     return QWEN35_OK;
 }
 
-// The layer tables live in device memory (the reference's packed blobs).  They are read back once
-// per distinct table pointer and kept on the host, as the reference does (prefill.cu:1179-1195).
-struct HostTables { const void* dev_layers; const void* dev_fused; LayerRec layers[NUM_LAYERS]; PrefillFused fused[NUM_LAYERS]; };
-static HostTables g_tables[8];
-static int g_tables_n = 0;
-static std::mutex g_tables_mu;
+// The layer tables live in device memory (the reference's packed blobs).  The reference reads them back once per
+// table pointer and keeps the copy (prefill.cu:1179-1195); a caller that frees and re-packs its weights can get the
+// same device address back with different contents, so here they are read back on every call (4 KB, a few
+// microseconds against a prefill of milliseconds).
+struct HostTables { LayerRec layers[NUM_LAYERS]; PrefillFused fused[NUM_LAYERS]; };
 
-static const HostTables* host_tables(const void* dev_layers, const void* dev_fused) {
-    std::lock_guard<std::mutex> lk(g_tables_mu);
-    for (int i = 0; i < g_tables_n; ++i)
-        if (g_tables[i].dev_layers == dev_layers && g_tables[i].dev_fused == dev_fused) return &g_tables[i];
-    HostTables* t = &g_tables[g_tables_n < 8 ? g_tables_n++ : 7];
-    t->dev_layers = dev_layers; t->dev_fused = dev_fused;
-    if (cudaMemcpy(t->layers, dev_layers, sizeof(t->layers), cudaMemcpyDeviceToHost) != cudaSuccess ||
-        cudaMemcpy(t->fused, dev_fused, sizeof(t->fused), cudaMemcpyDeviceToHost) != cudaSuccess) {
-        set_error("reading the layer tables failed");
-        t->dev_layers = nullptr;
-        return nullptr;
+static bool read_tables(HostTables* t, const void* dev_layers, const void* dev_fused, cudaStream_t stream) {
+    if (cudaMemcpyAsync(t->layers, dev_layers, sizeof(t->layers), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+        cudaMemcpyAsync(t->fused, dev_fused, sizeof(t->fused), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+        cudaStreamSynchronize(stream) != cudaSuccess) {
+        set_error("reading the layer tables failed: %s", cudaGetErrorString(cudaGetLastError()));
+        return false;
     }
-    return t;
+    return true;
 }
 
 }  // namespace q35
@@ -173,8 +167,9 @@ extern "C" int qwen35_b200_prefill_bf16(const Qwen35PrefillArgs* in, qwen35_stre
         set_error("null tensor pointer");
         return QWEN35_ERR_BAD_ARG;
     }
-    const HostTables* t = host_tables(in->layer_weights, in->fused_layer_weights);
-    if (!t) return QWEN35_ERR_CUDA;
+    HostTables tables;
+    const HostTables* t = &tables;
+    if (!read_tables(&tables, in->layer_weights, in->fused_layer_weights, (cudaStream_t)stream)) return QWEN35_ERR_CUDA;
     PrefillArgs a = {};
     a.token_ids = in->token_ids; a.S = in->seq_len; a.out_token = in->out_token;
     a.embed = (const bf16*)in->embed_weight; a.layers_host = t->layers; a.fused_host = t->fused;

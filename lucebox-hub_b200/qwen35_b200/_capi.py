@@ -55,6 +55,7 @@ class BatchedArgs(C.Structure):
         ("k_pages", C.c_void_p), ("v_pages", C.c_void_p), ("dn_states", C.c_void_p), ("conv_bufs", C.c_void_p),
         ("logits_out", C.c_void_p), ("dbg_hidden", C.c_void_p), ("dbg_teacher", C.c_void_p),
         ("advance_positions", C.c_int), ("dbg_num_layers", C.c_int),
+        ("layer_weights_host", C.c_void_p), ("fused_layer_weights_host", C.c_void_p),
     ]
 
 

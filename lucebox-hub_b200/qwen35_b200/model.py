@@ -445,6 +445,9 @@ class BatchedDecoder:
         _attach_prefill_fused_weights(weights)
         self._layer_weights_packed = _pack_layer_weights(weights["layer_data"], device)
         self._prefill_fused_weights_packed = _pack_prefill_fused_layer_weights(weights["prefill_fused_layer_data"], device)
+        # host copies of the two tables: with them a step never synchronises
+        self._layer_weights_host = self._layer_weights_packed.cpu()
+        self._fused_weights_host = self._prefill_fused_weights_packed.cpu()
         dev = self.device
         self.k_pages = torch.zeros(6, self.num_pages, FA_NUM_KV_HEADS, KV_PAGE, FA_HEAD_DIM, dtype=torch.bfloat16, device=dev)
         self.v_pages = torch.zeros_like(self.k_pages)
@@ -490,6 +493,7 @@ class BatchedDecoder:
         a.block_table = self.block_table.data_ptr()
         a.embed_weight = self._weights["embed_weight"].data_ptr(); a.layer_weights = self._layer_weights_packed.data_ptr()
         a.fused_layer_weights = self._prefill_fused_weights_packed.data_ptr()
+        a.layer_weights_host = self._layer_weights_host.data_ptr(); a.fused_layer_weights_host = self._fused_weights_host.data_ptr()
         a.final_norm_weight = self._weights["final_norm_weight"].data_ptr(); a.lm_head_weight = self._weights["lm_head_weight"].data_ptr()
         a.k_pages = self.k_pages.data_ptr(); a.v_pages = self.v_pages.data_ptr()
         a.dn_states = self.dn_states.data_ptr(); a.conv_bufs = self.conv_bufs.data_ptr()

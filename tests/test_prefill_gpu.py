@@ -45,7 +45,9 @@ def _gemm(A, B, N, epi=0, R=None, up_off=0):
     return out
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 64, 64), (7, 96, 128), (128, 128, 1024), (520, 8224, 1024), (333, 1024, 3584), (1024, 5120, 1024)])
+# single-row-of-tiles shapes (M <= 128) run the narrow 16/32/64-column tiles; the others the 128-column tile
+@pytest.mark.parametrize("M,N,K", [(1, 64, 64), (7, 96, 128), (128, 128, 1024), (520, 8224, 1024), (333, 1024, 3584), (1024, 5120, 1024),
+                                   (64, 1024, 2048), (64, 5120, 1024), (64, 8224, 1024), (33, 1000, 3584), (128, 20000, 1024)])
 def test_gemm_plain(M, N, K):
     torch.manual_seed(M * 7 + N)
     A = torch.randn(M, K, device="cuda").bfloat16()
@@ -66,14 +68,21 @@ def test_gemm_fused_epilogues():
     got = _gemm(A, B, N, epi=1, R=R)
     ref = (A.float() @ B.float().t()).bfloat16() + R
     assert float((got != ref).float().mean()) <= GEMM_FLIP_FRAC
-    M, N, K = 130, 3584, 1024
+    for M, N, K in ((130, 3584, 1024), (64, 3584, 1024), (64, 520, 1024), (16, 40, 128)):
+        A = torch.randn(M, K, device="cuda").bfloat16()
+        B = (torch.randn(2 * N, K, device="cuda") * 0.05).bfloat16()
+        got = _gemm(A, B, N, epi=2, up_off=N)
+        g = (A.float() @ B[:N].float().t()).bfloat16()
+        u = (A.float() @ B[N:].float().t()).bfloat16()
+        ref = torch.nn.functional.silu(g) * u
+        assert float((got != ref).float().mean()) <= 2 * GEMM_FLIP_FRAC, (M, N, K)
+    M, N, K = 64, 1024, 3584
     A = torch.randn(M, K, device="cuda").bfloat16()
-    B = (torch.randn(2 * N, K, device="cuda") * 0.05).bfloat16()
-    got = _gemm(A, B, N, epi=2, up_off=N)
-    g = (A.float() @ B[:N].float().t()).bfloat16()
-    u = (A.float() @ B[N:].float().t()).bfloat16()
-    ref = torch.nn.functional.silu(g) * u
-    assert float((got != ref).float().mean()) <= 2 * GEMM_FLIP_FRAC
+    B = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    R = torch.randn(M, N, device="cuda").bfloat16()
+    got = _gemm(A, B, N, epi=1, R=R)
+    ref = (A.float() @ B.float().t()).bfloat16() + R
+    assert float((got != ref).float().mean()) <= GEMM_FLIP_FRAC
 
 
 def test_gemm_rejects_bad_shapes():
