@@ -133,14 +133,14 @@ def batched_decode_bench(weights_gpu, dev, rank, n_seq, ctx, n_steps):
         bd.prefill(sq, make_token_ids(ctx, 1000 * rank + sq, D.vocab).to(dev))
     snap = [t.clone() for t in (bd.dn_states, bd.conv_bufs, bd.positions, bd.tokens)]
     for _ in range(3):
-        bd.step()
+        bd.step(graph=True)
     for dst, src in zip((bd.dn_states, bd.conv_bufs, bd.positions, bd.tokens), snap):
         dst.copy_(src)
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(n_steps):
-        bd.step()
+        bd.step(graph=True)
     e1.record()
     torch.cuda.synchronize(dev)
     bd.check_status()

@@ -34,25 +34,30 @@ __device__ __forceinline__ float conv_silu4(const bf16* conv_w, int ch, float4 s
     return rbf(silu_f(rbf(c)));
 }
 
-// ---- DeltaNet step: one CTA (128 threads) per (sequence, head, block of 16 value rows) ------------------
-__global__ void __launch_bounds__(128) bd_dn_step_kernel(const bf16* __restrict__ proj, int ldp, const bf16* __restrict__ conv_w,
+// ---- DeltaNet step: one CTA (256 threads) per (sequence, head, block of 64 value rows) -------------------
+constexpr int BD_DN_ROWS = 64;
+__global__ void __launch_bounds__(256) bd_dn_step_kernel(const bf16* __restrict__ proj, int ldp, const bf16* __restrict__ conv_w,
                                                          const bf16* __restrict__ a_log, const bf16* __restrict__ dt_bias,
                                                          const float* __restrict__ conv, size_t conv_seq_stride,
                                                          float* __restrict__ state, size_t state_seq_stride, bf16* __restrict__ core_out) {
-    __shared__ __align__(16) float sq[DN_K];
-    __shared__ __align__(16) float sk[DN_K];
+    __shared__ __align__(16) float sqk[2][DN_K];
     __shared__ float red[2][4];
     __shared__ float shd[2];
-    const int b = blockIdx.x, h = blockIdx.y, rb = blockIdx.z, i = threadIdx.x, warp = i >> 5, lane = i & 31;
+    __shared__ float svv[BD_DN_ROWS];
+    const int b = blockIdx.x, h = blockIdx.y, rb = blockIdx.z, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bf16* xrow = proj + (size_t)b * ldp;
     const float4* cv = reinterpret_cast<const float4*>(conv + (size_t)b * conv_seq_stride);
-    // q and k of this head: conv + SiLU, then the L2 norm in bf16 arithmetic (single-token form of the oracle)
-    const int chq = h * DN_K + i, chk = DN_QK_SIZE + h * DN_K + i;
-    const float cq = conv_silu4(conv_w, chq, cv[chq], bf2f(xrow[chq]));
-    const float ck = conv_silu4(conv_w, chk, cv[chk], bf2f(xrow[chk]));
-    const float s0 = warp_sum(rbf(cq * cq)), s1 = warp_sum(rbf(ck * ck));
-    if (lane == 0) { red[0][warp] = s0; red[1][warp] = s1; }
-    if (i == 0) {
+    // q (threads 0-127) and k (threads 128-255) of this head: conv + SiLU, then the L2 norm in bf16 arithmetic
+    const int which = tid >> 7, i = tid & 127;
+    const int chx = which * DN_QK_SIZE + h * DN_K + i;
+    const float cx = conv_silu4(conv_w, chx, cv[chx], bf2f(xrow[chx]));
+    const float s0 = warp_sum(rbf(cx * cx));
+    if (lane == 0) red[which][warp & 3] = s0;
+    if (tid < BD_DN_ROWS) {
+        const int ch = 2 * DN_QK_SIZE + h * DN_V + rb * BD_DN_ROWS + tid;
+        svv[tid] = conv_silu4(conv_w, ch, cv[ch], bf2f(xrow[ch]));
+    }
+    if (tid == 0) {
         const float bb = bf2f(xrow[DN_CONV_CH + DN_V_SIZE + h]);
         const float aa = bf2f(xrow[DN_CONV_CH + DN_V_SIZE + DN_HEADS + h]);
         const float x = aa + bf2f(dt_bias[h]);
@@ -62,34 +67,34 @@ __global__ void __launch_bounds__(128) bd_dn_step_kernel(const bf16* __restrict_
     }
     __syncthreads();
     {
-        float tq = ((red[0][0] + red[0][1]) + red[0][2]) + red[0][3];
-        float tk = ((red[1][0] + red[1][1]) + red[1][2]) + red[1][3];
-        tq = rbf(rbf(tq) + 1e-6f);
-        tk = rbf(rbf(tk) + 1e-6f);
-        sq[i] = rbf(cq * rbf(1.0f / rbf(sqrtf(tq)))) * 0.08838834764831845f;
-        sk[i] = rbf(ck * rbf(1.0f / rbf(sqrtf(tk))));
+        float t = ((red[which][0] + red[which][1]) + red[which][2]) + red[which][3];
+        t = rbf(rbf(t) + 1e-6f);
+        const float n = rbf(cx * rbf(1.0f / rbf(sqrtf(t))));
+        sqk[which][i] = which ? n : n * 0.08838834764831845f;
     }
     __syncthreads();
-    const float4 q4 = *reinterpret_cast<const float4*>(&sq[lane * 4]);
-    const float4 k4 = *reinterpret_cast<const float4*>(&sk[lane * 4]);
+    const float4 q4 = *reinterpret_cast<const float4*>(&sqk[0][lane * 4]);
+    const float4 k4 = *reinterpret_cast<const float4*>(&sqk[1][lane * 4]);
     const float beta = shd[0], decay = shd[1];
     float* st_base = state + (size_t)b * state_seq_stride + (size_t)h * DN_V * DN_K;
+    constexpr int RPW = BD_DN_ROWS / 8;                 // rows per warp
+    float4 t[RPW];
 #pragma unroll
-    for (int r = 0; r < 4; ++r) {
-        const int v = rb * 16 + warp * 4 + r;
-        const int ch = 2 * DN_QK_SIZE + h * DN_V + v;
-        const float vv = conv_silu4(conv_w, ch, cv[ch], bf2f(xrow[ch]));
-        float4* sp = reinterpret_cast<float4*>(st_base + (size_t)v * DN_K) + lane;
-        float4 t = *sp;
-        t.x = __fmul_rn(t.x, decay); t.y = __fmul_rn(t.y, decay); t.z = __fmul_rn(t.z, decay); t.w = __fmul_rn(t.w, decay);
-        float kv = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(t.x, k4.x), __fmul_rn(t.y, k4.y)), __fmul_rn(t.z, k4.z)), __fmul_rn(t.w, k4.w));
+    for (int r = 0; r < RPW; ++r)
+        t[r] = *(reinterpret_cast<const float4*>(st_base + (size_t)(rb * BD_DN_ROWS + warp * RPW + r) * DN_K) + lane);
+#pragma unroll
+    for (int r = 0; r < RPW; ++r) {
+        const int vl = warp * RPW + r, v = rb * BD_DN_ROWS + vl;
+        float4 u = t[r];
+        u.x = __fmul_rn(u.x, decay); u.y = __fmul_rn(u.y, decay); u.z = __fmul_rn(u.z, decay); u.w = __fmul_rn(u.w, decay);
+        float kv = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(u.x, k4.x), __fmul_rn(u.y, k4.y)), __fmul_rn(u.z, k4.z)), __fmul_rn(u.w, k4.w));
         kv = warp_sum(kv);
-        const float delta = __fmul_rn(__fsub_rn(vv, kv), beta);
-        t.x = __fadd_rn(t.x, __fmul_rn(k4.x, delta)); t.y = __fadd_rn(t.y, __fmul_rn(k4.y, delta));
-        t.z = __fadd_rn(t.z, __fmul_rn(k4.z, delta)); t.w = __fadd_rn(t.w, __fmul_rn(k4.w, delta));
-        float o = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(t.x, q4.x), __fmul_rn(t.y, q4.y)), __fmul_rn(t.z, q4.z)), __fmul_rn(t.w, q4.w));
+        const float delta = __fmul_rn(__fsub_rn(svv[vl], kv), beta);
+        u.x = __fadd_rn(u.x, __fmul_rn(k4.x, delta)); u.y = __fadd_rn(u.y, __fmul_rn(k4.y, delta));
+        u.z = __fadd_rn(u.z, __fmul_rn(k4.z, delta)); u.w = __fadd_rn(u.w, __fmul_rn(k4.w, delta));
+        float o = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(u.x, q4.x), __fmul_rn(u.y, q4.y)), __fmul_rn(u.z, q4.z)), __fmul_rn(u.w, q4.w));
         o = warp_sum(o);
-        *sp = t;
+        *(reinterpret_cast<float4*>(st_base + (size_t)v * DN_K) + lane) = u;
         if (lane == 0) core_out[(size_t)b * DN_V_SIZE + h * DN_V + v] = f2bf(o);
     }
 }
@@ -419,7 +424,7 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
             Q35_TRYB(gemm_bf16(normed, HIDDEN, (const bf16*)F.proj_weight, DN_PROJ_ROWS, proj, ldp, nullptr, 0, B, DN_PROJ_ROWS, HIDDEN, 0, 0, stream));
             float* conv = (float*)in->conv_bufs + (size_t)i_dn * DN_CONV_CH * 4;
             float* state = (float*)in->dn_states + (size_t)i_dn * DN_HEADS * DN_V * DN_K;
-            bd_dn_step_kernel<<<dim3(B, DN_HEADS, DN_V / 16), 128, 0, stream>>>(proj, ldp, (const bf16*)L.p[DN_CONV], (const bf16*)L.p[DN_ALOG],
+            bd_dn_step_kernel<<<dim3(B, DN_HEADS, DN_V / BD_DN_ROWS), 256, 0, stream>>>(proj, ldp, (const bf16*)L.p[DN_CONV], (const bf16*)L.p[DN_ALOG],
                                                                                   (const bf16*)L.p[DN_DTBIAS], conv, conv_stride, state, state_stride, core);
             bd_conv_shift_kernel<<<(B * DN_CONV_CH + 255) / 256, 256, 0, stream>>>(proj, ldp, conv, conv_stride, B);
             pf_gated_norm_kernel<<<(B * DN_HEADS + 7) / 8, 256, 0, stream>>>(core, proj, ldp, (const bf16*)L.p[DN_NORM], attn, B);

@@ -446,6 +446,7 @@ class BatchedDecoder:
         self._layer_weights_packed = _pack_layer_weights(weights["layer_data"], device)
         self._prefill_fused_weights_packed = _pack_prefill_fused_layer_weights(weights["prefill_fused_layer_data"], device)
         # host copies of the two tables: with them a step never synchronises
+        self._graph = None; self._warm = False
         self._layer_weights_host = self._layer_weights_packed.cpu()
         self._fused_weights_host = self._prefill_fused_weights_packed.cpu()
         dev = self.device
@@ -502,13 +503,27 @@ class BatchedDecoder:
             setattr(a, k, v)
         return a
 
-    def step(self, **kw):
-        """One greedy token for every sequence; the new tokens become the next step's inputs.  Returns int32 [batch] (GPU)."""
-        a = self._args(**{k: (_capi.ptr(v) if torch.is_tensor(v) else v) for k, v in kw.items()})
+    def _launch(self, a):
         with torch.cuda.device(self.device):
             _capi.check(self._lib.qwen35_b200_decode_batched(C.byref(a), C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)),
                         "decode_batched")
-        self.tokens, self._out = self._out, self.tokens
+            self.tokens.copy_(self._out)
+
+    def step(self, graph=False, **kw):
+        """One greedy token for every sequence; the new tokens become the next step's inputs.  Returns int32 [batch]
+        (GPU; the same buffer every step: clone it to keep a value).  graph=True replays a CUDA graph of the step's
+        launches (recorded on the second such call: the first runs eagerly so the library's scratch exists)."""
+        if graph and not kw:
+            if self._graph is None and self._warm:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.device(self.device), torch.cuda.graph(g):
+                    self._launch(self._args())
+                self._graph = g
+            if self._graph is not None:
+                self._graph.replay()
+                return self.tokens
+        self._launch(self._args(**{k: (_capi.ptr(v) if torch.is_tensor(v) else v) for k, v in kw.items()}))
+        self._warm = True
         return self.tokens
 
     def check_status(self):

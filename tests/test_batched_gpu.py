@@ -77,3 +77,20 @@ def test_batched_free_running_and_prefill(full_weights_cpu):
     assert torch.equal(outs[:, 0], outs[:, 1]) and torch.equal(outs[:, 0], outs[:, 3])      # identical sequences stay identical
     assert bool(((outs >= 0) & (outs < D.vocab)).all())
     assert bd.positions.tolist() == [46, 46, 39, 46]
+
+
+def test_batched_graph_replay_equals_eager(full_weights_cpu):
+    """step(graph=True) replays a CUDA graph of the same launches: tokens, positions and states equal the eager run."""
+    from qwen35_b200.config import QWEN35_0P8B as D
+    from qwen35_b200.model import BatchedDecoder
+    from qwen35_b200.weights import make_token_ids, weights_to
+    wg = weights_to(full_weights_cpu, "cuda")
+    runs = []
+    for use_graph in (False, True):
+        bd = BatchedDecoder(wg, batch=3, max_ctx=192)
+        for b in range(3):
+            bd.prefill(b, make_token_ids(20 + 30 * b, 9 + b, D.vocab).cuda())
+        outs = torch.stack([bd.step(graph=use_graph).clone() for _ in range(5)])
+        bd.check_status()
+        runs.append((outs.cpu(), bd.positions.cpu(), bd.dn_states.cpu()))
+    assert torch.equal(runs[0][0], runs[1][0]) and torch.equal(runs[0][1], runs[1][1]) and torch.equal(runs[0][2], runs[1][2])
