@@ -199,8 +199,8 @@ int launch_quantize_nvfp4_lm_out(const void* weight, int rows, int cols, void* p
  * max_ctx bounds positions+1 (<= 8192).  advance_positions != 0 increments positions[] on the device after the
  * step, so steps chain without host work.  Weights are the bf16 tables of launch_prefill_bf16.
  * layer_weights_host / fused_layer_weights_host: optional host copies of the two device tables (same bytes).  With
- * them the call never synchronises, so steps can be queued back to back; without them it reads the device tables
- * back on every call (a stream synchronisation per step). */
+ * them no call ever synchronises; without them the first call with a new pair of device tables reads them back
+ * (see qwen35_b200_forget_tables). */
 typedef struct {
     int batch; int max_ctx; int num_pages; int max_pages;
     const int* tokens_in; int* tokens_out; int* positions; const int* block_table;
@@ -215,6 +215,12 @@ typedef struct {
     const void* layer_weights_host; const void* fused_layer_weights_host;
 } Qwen35BatchedArgs;
 int qwen35_b200_decode_batched(const Qwen35BatchedArgs* args, qwen35_stream_t stream);
+
+/* The prefill and batched-decode entry points keep a host copy of the device pointer tables, keyed by the two
+ * table addresses, exactly as the reference keeps its host copy (prefill.cu:1179-1195): after the first call they
+ * neither synchronise nor allocate.  A caller that frees its tables and packs new ones may get the same addresses
+ * back; it calls this after re-packing so the next call reads the tables again.  No reference counterpart. */
+void qwen35_b200_forget_tables(void);
 
 /* BF16 GEMM on tcgen05/TMEM tensor cores: C[M,N] = epi(A[M,K] . B[b_rows,K]^T), f32 accumulate, one
  * rounding to bf16.  Replaces cublas_bf16_gemm (prefill.cu:895-903).  lda/ldc/ldr are row strides in

@@ -344,7 +344,7 @@ static void* batched_scratch(size_t bytes) {
 }
 
 struct PrefillFusedB { const void* proj_weight; const void* gate_up_weight; const void* unused[4]; };
-struct HostTablesB { LayerRec layers[NUM_LAYERS]; PrefillFusedB fused[NUM_LAYERS]; };
+const void* host_layer_tables(const void* dev_layers, const void* dev_fused, const void** fused_out);
 
 }  // namespace q35
 
@@ -368,20 +368,15 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
         set_error("null tensor pointer");
         return QWEN35_ERR_BAD_ARG;
     }
-    // Layer tables on the host: the caller's host copies when given (no synchronisation: steps can be queued
-    // back to back), else read back from the device tables on every call (never cached: a re-packed table can
-    // come back at the same device address).
-    HostTablesB tables;
+    // Layer tables on the host: the caller's host copies when given, else the library's copy of the device tables
+    // (read back once per pair of table pointers, as for prefill)
     const LayerRec* layers_h = reinterpret_cast<const LayerRec*>(in->layer_weights_host);
     const PrefillFusedB* fused_h = reinterpret_cast<const PrefillFusedB*>(in->fused_layer_weights_host);
     if (!layers_h || !fused_h) {
-        if (cudaMemcpyAsync(tables.layers, in->layer_weights, sizeof(tables.layers), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
-            cudaMemcpyAsync(tables.fused, in->fused_layer_weights, sizeof(tables.fused), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
-            cudaStreamSynchronize(stream) != cudaSuccess) {
-            set_error("reading the layer tables failed: %s", cudaGetErrorString(cudaGetLastError()));
-            return QWEN35_ERR_CUDA;
-        }
-        layers_h = tables.layers; fused_h = tables.fused;
+        const void* f = nullptr;
+        layers_h = reinterpret_cast<const LayerRec*>(host_layer_tables(in->layer_weights, in->fused_layer_weights, &f));
+        fused_h = reinterpret_cast<const PrefillFusedB*>(f);
+        if (!layers_h) return QWEN35_ERR_CUDA;
     }
     // scratch rows of B tokens
     const size_t rows = (size_t)B;

@@ -9,6 +9,12 @@
 //              stage) and commits each stage back to the producer
 //   warps 2-5  epilogue: tcgen05.ld the accumulator rows, round once to bf16 (what a bf16 linear
 //              layer returns), optionally fuse the residual add or silu(gate)*up, store
+// A skinny problem (M <= 128 rows of activations against a tall weight matrix) is bound by the fixed cost of a
+// k-step (barrier hand-offs: about 0.3 us whatever the tile holds), not by bytes or flops, so it runs split along
+// K: a thread-block cluster of S CTAs shares one 128 x 128 output tile, each CTA accumulates its slice of K in
+// TMEM, parks the f32 tile in its own shared memory, and after a cluster barrier CTA r sums columns
+// [r*128/S, (r+1)*128/S) over all peers through distributed shared memory (fixed order: deterministic) and
+// applies the epilogue.  No partial sums go through global memory and no second kernel runs.
 // Every wait is bounded; a wait that runs out sets the status word and the CTA unwinds normally.
 #include <cuda.h>
 
@@ -17,13 +23,15 @@
 
 namespace q35 {
 
-constexpr int GEMM_BM = 128, GEMM_BK = 64;
+constexpr int GEMM_BM = 128, GEMM_BN = 128, GEMM_BK = 64;
 constexpr int GEMM_THREADS = 192;
-__host__ __device__ constexpr int gemm_stages(int bn) { return bn == 128 ? 6 : 4; }          // narrow tiles: two CTAs per SM
-__host__ __device__ constexpr uint32_t gemm_stage_bytes(int bn) { return (uint32_t)(GEMM_BM + bn) * GEMM_BK * 2; }
-__host__ __device__ constexpr uint32_t gemm_smem(int bn) { return gemm_stages(bn) * gemm_stage_bytes(bn) + 1024 /*align*/ + 256 /*barriers*/; }
+constexpr uint32_t GEMM_STAGE_BYTES = (GEMM_BM + GEMM_BN) * GEMM_BK * 2;   // 32 KB
+// 6 stages for the wide problems (one CTA per SM); the skinny ones run a few k-steps per CTA: 3 stages, two CTAs per SM
+constexpr int GEMM_STAGES_WIDE = 6, GEMM_STAGES_SKINNY = 3;
+__host__ __device__ constexpr uint32_t gemm_smem(int stages) { return stages * GEMM_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/; }
+static_assert(GEMM_STAGES_SKINNY * GEMM_STAGE_BYTES >= GEMM_BM * GEMM_BN * 4, "the parked f32 tile reuses the stage buffers");
+constexpr int GEMM_MAX_SPLIT = 8;        // portable cluster size
 constexpr unsigned GEMM_SPIN_LIMIT = 20u * 1000u * 1000u;
-
 enum GemmEpi { EPI_BF16 = 0, EPI_RESIDUAL = 1, EPI_SILU_MUL = 2 };
 
 struct GemmParams {
@@ -77,7 +85,7 @@ __device__ __forceinline__ uint64_t make_smem_desc(uint32_t smem_addr) {
     return d;
 }
 // instruction descriptor: D f32, A/B bf16, both K-major, N at [17,23) in units of 8, M at [24,29) in units of 16
-__host__ __device__ constexpr uint32_t gemm_idesc(int bn) { return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(GEMM_BM >> 4) << 24); }
+constexpr uint32_t GEMM_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(GEMM_BN >> 3) << 17) | ((uint32_t)(GEMM_BM >> 4) << 24);
 
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
     asm volatile(
@@ -100,57 +108,88 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         : "r"(taddr) : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr) : "memory");
+// ---- cluster helpers (split-K) ----
+__device__ __forceinline__ uint32_t cluster_ctarank() { uint32_t r; asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r)); return r; }
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t* r) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-        : "r"(taddr) : "memory");
+__device__ __forceinline__ uint32_t map_to_cta(uint32_t local_smem_addr, uint32_t cta) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(cta));
+    return r;
 }
-// W accumulator columns of this thread's TMEM lane, W = 8, 16 or 32
-template <int W>
-__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[32]) {
-    if (W == 32) tmem_ld32(taddr, r);
-    else if (W == 16) tmem_ld16(taddr, r);
-    else tmem_ld8(taddr, r);
+__device__ __forceinline__ float ld_dsmem(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+    return v;
 }
 
-template <int EPI, int GEMM_BN>
+// epilogue arithmetic on 8 adjacent output columns of one row; acc = f32 sums (SILU: gate then up), one 16-byte store
+template <int EPI>
+__device__ __forceinline__ void epilogue_store8(const GemmParams& p, int row, int n, const float* g, const float* u) {
+    float y[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        if (EPI == EPI_SILU_MUL) y[j] = rbf(silu_f(rbf(g[j]))) * rbf(u[j]);
+        else y[j] = rbf(g[j]);
+    }
+    bf16* dst = p.C + (size_t)row * p.ldc + n;
+    if (n + 8 <= p.N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) && (EPI != EPI_RESIDUAL || ((reinterpret_cast<uintptr_t>(p.R + (size_t)row * p.ldr + n) & 15) == 0))) {
+        if (EPI == EPI_RESIDUAL) {
+            const uint4 r = *reinterpret_cast<const uint4*>(p.R + (size_t)row * p.ldr + n);
+            y[0] += bf_lo(r.x); y[1] += bf_hi(r.x); y[2] += bf_lo(r.y); y[3] += bf_hi(r.y);
+            y[4] += bf_lo(r.z); y[5] += bf_hi(r.z); y[6] += bf_lo(r.w); y[7] += bf_hi(r.w);
+        }
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const __nv_bfloat162 pr = __halves2bfloat162(f2bf(y[2 * j]), f2bf(y[2 * j + 1]));
+            o[j] = *reinterpret_cast<const uint32_t*>(&pr);
+        }
+        *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (n + j < p.N) {
+                float v = y[j];
+                if (EPI == EPI_RESIDUAL) v += bf2f(p.R[(size_t)row * p.ldr + n + j]);
+                dst[j] = f2bf(v);
+            }
+    }
+}
+
+// SPLIT: gridDim.z = cluster size S along K (1, 2, 4 or 8); the cluster shares one output tile
+template <int EPI, int STAGES, bool SPLIT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
 gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
-    constexpr int GEMM_STAGES = gemm_stages(GEMM_BN);
-    constexpr uint32_t GEMM_STAGE_BYTES = gemm_stage_bytes(GEMM_BN), GEMM_IDESC = gemm_idesc(GEMM_BN);
-    constexpr uint32_t TMEM_COLS = GEMM_BN < 32 ? 32u : (uint32_t)GEMM_BN;
-    constexpr int HALF = GEMM_BN / 2;          // B rows per TMA box
     extern __shared__ unsigned char g_smem_raw[];
     // 128B-swizzled tiles need 1024-byte alignment
     const uint32_t raw = g_smem_u32(g_smem_raw);
     const uint32_t tiles = (raw + 1023u) & ~1023u;
     unsigned char* tiles_ptr = g_smem_raw + (tiles - raw);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(tiles_ptr + GEMM_STAGES * GEMM_STAGE_BYTES);
-    const uint32_t full0 = g_smem_u32(bars), empty0 = full0 + 8 * GEMM_STAGES, tfull = empty0 + 8 * GEMM_STAGES;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * GEMM_STAGES + 1);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(tiles_ptr + STAGES * GEMM_STAGE_BYTES);
+    const uint32_t full0 = g_smem_u32(bars), empty0 = full0 + 8 * STAGES, tfull = empty0 + 8 * STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
     volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int BN_OUT = (EPI == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
     const int n0 = blockIdx.x * BN_OUT, m0 = blockIdx.y * GEMM_BM;
-    const int nkb = p.K / GEMM_BK;
+    const int nkb_all = p.K / GEMM_BK;
+    const int S = SPLIT ? (int)gridDim.z : 1, z = SPLIT ? (int)blockIdx.z : 0;
+    const int kb_begin = (int)(((long long)z * nkb_all) / S), kb_end = (int)(((long long)(z + 1) * nkb_all) / S);
+    const int nkb = kb_end - kb_begin;
 
     if (threadIdx.x == 0) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmB) : "memory");
         *s_abort = 0;
-        for (int i = 0; i < GEMM_STAGES; ++i) { g_mbar_init(full0 + 8 * i, 1); g_mbar_init(empty0 + 8 * i, 1); }
+        for (int i = 0; i < STAGES; ++i) { g_mbar_init(full0 + 8 * i, 1); g_mbar_init(empty0 + 8 * i, 1); }
         g_mbar_init(tfull, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(g_smem_u32(tmem_slot)), "r"(TMEM_COLS) : "memory");
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(g_smem_u32(tmem_slot)), "r"(128u) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -161,37 +200,37 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
     if (warp == 0) {
         if (lane == 0) {
             int issued = 0;
-            for (int kb = 0; kb < nkb; ++kb) {
-                const int st = kb % GEMM_STAGES;
-                if (!g_mbar_wait(empty0 + 8 * st, ((kb / GEMM_STAGES) & 1) ^ 1, p.err, s_abort)) break;
+            for (int i = 0; i < nkb; ++i) {
+                const int st = i % STAGES, kb = kb_begin + i;
+                if (!g_mbar_wait(empty0 + 8 * st, ((i / STAGES) & 1) ^ 1, p.err, s_abort)) break;
                 const uint32_t a_dst = tiles + st * GEMM_STAGE_BYTES, b_dst = a_dst + GEMM_BM * GEMM_BK * 2;
                 g_mbar_expect_tx(full0 + 8 * st, GEMM_STAGE_BYTES);
                 g_tma_load_2d(a_dst, &tmA, kb * GEMM_BK, m0, full0 + 8 * st);
                 g_tma_load_2d(b_dst, &tmB, kb * GEMM_BK, n0, full0 + 8 * st);
-                g_tma_load_2d(b_dst + HALF * GEMM_BK * 2, &tmB, kb * GEMM_BK, (EPI == EPI_SILU_MUL ? p.up_row_offset : HALF) + n0, full0 + 8 * st);
-                issued = kb + 1;
+                g_tma_load_2d(b_dst + 64 * GEMM_BK * 2, &tmB, kb * GEMM_BK, (EPI == EPI_SILU_MUL ? p.up_row_offset : 64) + n0, full0 + 8 * st);
+                issued = i + 1;
             }
             // every copy this CTA issued must have landed before it may exit (matters only after an abort)
             if (*s_abort) {
-                for (int kb = max(0, issued - GEMM_STAGES); kb < issued; ++kb) {
+                for (int i = max(0, issued - STAGES); i < issued; ++i) {
                     unsigned it = 0;
-                    while (!g_mbar_try_wait(full0 + 8 * (kb % GEMM_STAGES), (kb / GEMM_STAGES) & 1) && ++it < GEMM_SPIN_LIMIT) {}
+                    while (!g_mbar_try_wait(full0 + 8 * (i % STAGES), (i / STAGES) & 1) && ++it < GEMM_SPIN_LIMIT) {}
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             bool ok = true;
-            for (int kb = 0; kb < nkb && ok; ++kb) {
-                const int st = kb % GEMM_STAGES;
-                ok = g_mbar_wait(full0 + 8 * st, (kb / GEMM_STAGES) & 1, p.err, s_abort);
+            for (int i = 0; i < nkb && ok; ++i) {
+                const int st = i % STAGES;
+                ok = g_mbar_wait(full0 + 8 * st, (i / STAGES) & 1, p.err, s_abort);
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t a_addr = tiles + st * GEMM_STAGE_BYTES, b_addr = a_addr + GEMM_BM * GEMM_BK * 2;
                 const uint64_t adesc = make_smem_desc(a_addr), bdesc = make_smem_desc(b_addr);
 #pragma unroll
                 for (int k = 0; k < GEMM_BK / 16; ++k)   // 32 bytes of K per instruction: advance the start-address field by 2
-                    umma_bf16(tmem_base, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), GEMM_IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+                    umma_bf16(tmem_base, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), GEMM_IDESC, (i > 0 || k > 0) ? 1u : 0u);
                 umma_commit(empty0 + 8 * st);       // frees the stage when these MMAs have read it
             }
             umma_commit(tfull);                     // accumulator complete (also fires after an abort so the epilogue wakes)
@@ -199,61 +238,100 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
     } else {
         // ---- epilogue: warp w may touch TMEM lanes [32*(w%4), +32) ----
         const int q = warp & 3;
-        const int row = m0 + q * 32 + lane;
-        const bool ok = g_mbar_wait(tfull, 0, p.err, s_abort) && !*s_abort;
+        const int rloc = q * 32 + lane, row = m0 + rloc;
+        // warp-uniform, because tcgen05.ld is a warp-wide instruction
+        const bool ok = __all_sync(0xffffffffu, g_mbar_wait(tfull, 0, p.err, s_abort) && !*s_abort);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        if (ok) {
-            if (EPI == EPI_SILU_MUL) {
-                constexpr int CW = HALF < 32 ? HALF : 32;      // gate columns [0, HALF), up columns [HALF, BN)
+        if (SPLIT) {
+            // park the f32 tile column-major in the (now idle) stage buffers: [column][row], conflict-free for a warp
+            float* park = reinterpret_cast<float*>(tiles_ptr);
 #pragma unroll
-                for (int c = 0; c < HALF / CW; ++c) {
-                    uint32_t g[32], u[32];
-                    tmem_ld<CW>(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * CW), g);
-                    tmem_ld<CW>(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(HALF + c * CW), u);
+            for (int c = 0; c < GEMM_BN / 32; ++c) {
+                if (m0 + q * 32 >= p.M) break;                  // rows of this warp are never read back
+                uint32_t v[32];
+                if (ok) {
+                    tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                    if (row < p.M) {
-                        bf16* dst = p.C + (size_t)row * p.ldc + n0 + c * CW;
-#pragma unroll
-                        for (int j = 0; j < CW; j += 2) {
-                            const int n = n0 + c * CW + j;
-                            const float m0v = rbf(silu_f(rbf(__uint_as_float(g[j])))) * rbf(__uint_as_float(u[j]));
-                            const float m1v = rbf(silu_f(rbf(__uint_as_float(g[j + 1])))) * rbf(__uint_as_float(u[j + 1]));
-                            if (n + 1 < p.N) *reinterpret_cast<__nv_bfloat162*>(dst + j) = __halves2bfloat162(f2bf(m0v), f2bf(m1v));
-                            else if (n < p.N) dst[j] = f2bf(m0v);
-                        }
-                    }
                 }
-            } else {
-                constexpr int CW = GEMM_BN < 32 ? GEMM_BN : 32;
 #pragma unroll
-                for (int c = 0; c < GEMM_BN / CW; ++c) {
-                    uint32_t v[32];
-                    tmem_ld<CW>(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * CW), v);
-                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                    if (row < p.M) {
-                        bf16* dst = p.C + (size_t)row * p.ldc + n0 + c * CW;
-                        const bf16* res = (EPI == EPI_RESIDUAL) ? p.R + (size_t)row * p.ldr + n0 + c * CW : nullptr;
+                for (int j = 0; j < 32; ++j) park[(c * 32 + j) * GEMM_BM + rloc] = ok ? __uint_as_float(v[j]) : 0.f;
+            }
+        } else if (ok) {
 #pragma unroll
-                        for (int j = 0; j < CW; j += 2) {
-                            const int n = n0 + c * CW + j;
-                            float y0 = rbf(__uint_as_float(v[j])), y1 = rbf(__uint_as_float(v[j + 1]));
-                            if (EPI == EPI_RESIDUAL) {
-                                if (n < p.N) y0 += bf2f(res[j]);
-                                if (n + 1 < p.N) y1 += bf2f(res[j + 1]);
-                            }
-                            if (n + 1 < p.N) *reinterpret_cast<__nv_bfloat162*>(dst + j) = __halves2bfloat162(f2bf(y0), f2bf(y1));
-                            else if (n < p.N) dst[j] = f2bf(y0);
-                        }
+            for (int c = 0; c < BN_OUT / 32; ++c) {
+                uint32_t g[32], u[32];
+                tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), g);
+                if (EPI == EPI_SILU_MUL) tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(64 + c * 32), u);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (row < p.M) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 8) {
+                        float gf[8], uf[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) { gf[e] = __uint_as_float(g[j + e]); uf[e] = (EPI == EPI_SILU_MUL) ? __uint_as_float(u[j + e]) : 0.f; }
+                        epilogue_store8<EPI>(p, row, n0 + c * 32 + j, gf, uf);
                     }
                 }
             }
         }
     }
+    if (SPLIT) {
+        // every thread of every CTA of the cluster passes both barriers, whatever happened above
+        __syncwarp();
+        cluster_sync_all();
+        if (warp >= 2 && !*s_abort) {
+            const uint32_t rank = cluster_ctarank();
+            const int slice = BN_OUT / S;                       // output columns this CTA finishes (a multiple of 8)
+            const int rows = min(GEMM_BM, p.M - m0);
+            const uint32_t park_local = tiles;
+            for (int item = (int)threadIdx.x - 64; item < rows * (slice / 8); item += GEMM_THREADS - 64) {
+                const int r = item % rows, cg = item / rows;
+                const int col = (int)rank * slice + cg * 8;     // first of 8 output columns within the tile
+                float g[8], u[8];
+                // all peers' values are requested before the first is used (one remote round trip, not S), then
+                // summed in peer order: the result does not depend on timing
+                float v[GEMM_MAX_SPLIT][8];
+#pragma unroll
+                for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
+                    if (peer < S) {
+                        const uint32_t base = map_to_cta(park_local, (uint32_t)peer);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) v[peer][e] = ld_dsmem(base + (uint32_t)(((col + e) * GEMM_BM + r) * 4));
+                    }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) { g[e] = 0.f; u[e] = 0.f; }
+#pragma unroll
+                for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
+                    if (peer < S) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) g[e] += v[peer][e];
+                    }
+                if (EPI == EPI_SILU_MUL) {
+#pragma unroll
+                    for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
+                        if (peer < S) {
+                            const uint32_t base = map_to_cta(park_local, (uint32_t)peer);
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) v[peer][e] = ld_dsmem(base + (uint32_t)(((64 + col + e) * GEMM_BM + r) * 4));
+                        }
+#pragma unroll
+                    for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
+                        if (peer < S) {
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) u[e] += v[peer][e];
+                        }
+                }
+                epilogue_store8<EPI>(p, m0 + r, n0 + col, g, u);
+            }
+        }
+        __syncwarp();
+        cluster_sync_all();                                     // no CTA leaves while a peer may still read its tile
+    }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 1) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(128u) : "memory");
     }
 }
 
@@ -298,38 +376,75 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
     void* ws = get_workspace();
     if (!ws) return QWEN35_ERR_CUDA;
     if (epi < 0 || epi > 2) { set_error("gemm_bf16: unknown epilogue %d", epi); return QWEN35_ERR_BAD_ARG; }
-    // tile width: 128 unless the problem is a single row of tiles, then the widest tile that still fills the SMs
-    const int m_tiles = (M + GEMM_BM - 1) / GEMM_BM;
-    int bn = 128;
-    if (m_tiles == 1) {
-        const int want = 120;
-        while (bn > 16 && (N + (epi == EPI_SILU_MUL ? bn / 2 : bn) - 1) / (epi == EPI_SILU_MUL ? bn / 2 : bn) < want) bn >>= 1;
-    }
     CUtensorMap tmA, tmB;
-    if (!make_tmap(&tmA, A, M, K, lda, GEMM_BM) || !make_tmap(&tmB, B, b_rows, K, K, bn / 2)) {
-        set_error("cuTensorMapEncodeTiled failed (A %p [%d x %d] ld %d; B %p [%d x %d] box rows %d)", (const void*)A, M, K, lda, (const void*)B, b_rows, K, bn / 2);
+    if (!make_tmap(&tmA, A, M, K, lda, GEMM_BM) || !make_tmap(&tmB, B, b_rows, K, K, 64)) {
+        set_error("cuTensorMapEncodeTiled failed (A %p [%d x %d] ld %d; B %p [%d x %d])", (const void*)A, M, K, lda, (const void*)B, b_rows, K);
         return QWEN35_ERR_CUDA;
     }
     GemmParams p{M, N, K, C, ldc, R, ldr, up_row_offset, (int*)ws};
-    const int bn_out = (epi == EPI_SILU_MUL) ? bn / 2 : bn;
-    dim3 grid((N + bn_out - 1) / bn_out, m_tiles);
-#define Q35_GEMM_CASE(E, BN)                                                                                                          \
-    case (E) * 1000 + (BN): {                                                                                                         \
-        static bool attr = false;                                                                                                     \
-        if (!attr) {                                                                                                                  \
-            Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<E, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem(BN))); \
-            attr = true;                                                                                                              \
-        }                                                                                                                             \
-        gemm_bf16_tcgen05_kernel<E, BN><<<grid, GEMM_THREADS, gemm_smem(BN), stream>>>(tmA, tmB, p);                                   \
-        break;                                                                                                                        \
+    const int bn_out = (epi == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
+    const int m_tiles = (M + GEMM_BM - 1) / GEMM_BM, n_tiles = (N + bn_out - 1) / bn_out, nkb = K / GEMM_BK;
+    if (m_tiles > 1) {
+        dim3 grid(n_tiles, m_tiles);
+#define Q35_GEMM_WIDE(E)                                                                                                                      \
+    case E: {                                                                                                                                 \
+        static bool attr = false;                                                                                                             \
+        if (!attr) {                                                                                                                          \
+            Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_WIDE, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                             (int)gemm_smem(GEMM_STAGES_WIDE)));                                                              \
+            attr = true;                                                                                                                      \
+        }                                                                                                                                     \
+        gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_WIDE, false><<<grid, GEMM_THREADS, gemm_smem(GEMM_STAGES_WIDE), stream>>>(tmA, tmB, p);        \
+        break;                                                                                                                                \
     }
-    switch (epi * 1000 + bn) {
-        Q35_GEMM_CASE(EPI_BF16, 128) Q35_GEMM_CASE(EPI_BF16, 64) Q35_GEMM_CASE(EPI_BF16, 32) Q35_GEMM_CASE(EPI_BF16, 16)
-        Q35_GEMM_CASE(EPI_RESIDUAL, 128) Q35_GEMM_CASE(EPI_RESIDUAL, 64) Q35_GEMM_CASE(EPI_RESIDUAL, 32) Q35_GEMM_CASE(EPI_RESIDUAL, 16)
-        Q35_GEMM_CASE(EPI_SILU_MUL, 128) Q35_GEMM_CASE(EPI_SILU_MUL, 64) Q35_GEMM_CASE(EPI_SILU_MUL, 32) Q35_GEMM_CASE(EPI_SILU_MUL, 16)
-        default: set_error("gemm_bf16: no kernel for epilogue %d, tile %d", epi, bn); return QWEN35_ERR_BAD_ARG;
+        switch (epi) { Q35_GEMM_WIDE(EPI_BF16) Q35_GEMM_WIDE(EPI_RESIDUAL) Q35_GEMM_WIDE(EPI_SILU_MUL) }
+#undef Q35_GEMM_WIDE
+    } else {
+        // one row of tiles: split K over a cluster until about one CTA per SM exists, at least two k-steps per CTA
+        int split = 1;
+        while (split < GEMM_MAX_SPLIT && n_tiles * split < 120 && nkb / (split * 2) >= 2) split *= 2;
+        if (split == 1) {
+            dim3 grid(n_tiles, 1);
+#define Q35_GEMM_ROW(E)                                                                                                                         \
+    case E: {                                                                                                                                   \
+        static bool attr = false;                                                                                                               \
+        if (!attr) {                                                                                                                            \
+            Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                             (int)gemm_smem(GEMM_STAGES_SKINNY)));                                                              \
+            attr = true;                                                                                                                        \
+        }                                                                                                                                       \
+        gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, false><<<grid, GEMM_THREADS, gemm_smem(GEMM_STAGES_SKINNY), stream>>>(tmA, tmB, p);      \
+        break;                                                                                                                                  \
     }
-#undef Q35_GEMM_CASE
+            switch (epi) { Q35_GEMM_ROW(EPI_BF16) Q35_GEMM_ROW(EPI_RESIDUAL) Q35_GEMM_ROW(EPI_SILU_MUL) }
+#undef Q35_GEMM_ROW
+            Q35_CUDA_OK(cudaGetLastError());
+            g_launches.fetch_add(1);
+            return QWEN35_OK;
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(n_tiles, 1, split);
+        cfg.blockDim = dim3(GEMM_THREADS);
+        cfg.dynamicSmemBytes = gemm_smem(GEMM_STAGES_SKINNY);
+        cfg.stream = stream;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 1; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = (unsigned)split;
+        cfg.attrs = at; cfg.numAttrs = 1;
+#define Q35_GEMM_SKINNY(E)                                                                                                                       \
+    case E: {                                                                                                                                    \
+        static bool attr = false;                                                                                                                \
+        if (!attr) {                                                                                                                             \
+            Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
+                                             (int)gemm_smem(GEMM_STAGES_SKINNY)));                                                               \
+            attr = true;                                                                                                                         \
+        }                                                                                                                                        \
+        Q35_CUDA_OK(cudaLaunchKernelEx(&cfg, gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, true>, tmA, tmB, p));                                \
+        break;                                                                                                                                   \
+    }
+        switch (epi) { Q35_GEMM_SKINNY(EPI_BF16) Q35_GEMM_SKINNY(EPI_RESIDUAL) Q35_GEMM_SKINNY(EPI_SILU_MUL) }
+#undef Q35_GEMM_SKINNY
+    }
     Q35_CUDA_OK(cudaGetLastError());
     g_launches.fetch_add(1);
     return QWEN35_OK;

@@ -138,23 +138,40 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
     return QWEN35_OK;
 }
 
-// The layer tables live in device memory (the reference's packed blobs).  The reference reads them back once per
-// table pointer and keeps the copy (prefill.cu:1179-1195); a caller that frees and re-packs its weights can get the
-// same device address back with different contents, so here they are read back on every call (4 KB, a few
-// microseconds against a prefill of milliseconds).
-struct HostTables { LayerRec layers[NUM_LAYERS]; PrefillFused fused[NUM_LAYERS]; };
+// The layer tables live in device memory (the reference's packed blobs).  As in the reference (prefill.cu:1179-1195)
+// they are read back once per distinct pair of table pointers and kept on the host, so later calls neither
+// synchronise nor allocate (a prefill can then be captured in a CUDA graph).  A caller that frees its tables and
+// packs new ones can get the same device address back with different contents: it calls
+// qwen35_b200_forget_tables() after re-packing (the Python host does so whenever it packs).
+struct HostTables { const void* dev_layers; const void* dev_fused; LayerRec layers[NUM_LAYERS]; PrefillFused fused[NUM_LAYERS]; };
+static HostTables g_tables[8];
+static int g_tables_n = 0;
+static std::mutex g_tables_mu;
 
-static bool read_tables(HostTables* t, const void* dev_layers, const void* dev_fused, cudaStream_t stream) {
-    if (cudaMemcpyAsync(t->layers, dev_layers, sizeof(t->layers), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
-        cudaMemcpyAsync(t->fused, dev_fused, sizeof(t->fused), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
-        cudaStreamSynchronize(stream) != cudaSuccess) {
+const void* host_layer_tables(const void* dev_layers, const void* dev_fused, const void** fused_out) {
+    std::lock_guard<std::mutex> lk(g_tables_mu);
+    for (int i = 0; i < g_tables_n; ++i)
+        if (g_tables[i].dev_layers == dev_layers && g_tables[i].dev_fused == dev_fused) { *fused_out = g_tables[i].fused; return g_tables[i].layers; }
+    HostTables* t = &g_tables[g_tables_n < 8 ? g_tables_n++ : 7];
+    t->dev_layers = dev_layers; t->dev_fused = dev_fused;
+    if (cudaMemcpy(t->layers, dev_layers, sizeof(t->layers), cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemcpy(t->fused, dev_fused, sizeof(t->fused), cudaMemcpyDeviceToHost) != cudaSuccess) {
         set_error("reading the layer tables failed: %s", cudaGetErrorString(cudaGetLastError()));
-        return false;
+        t->dev_layers = nullptr;
+        return nullptr;
     }
-    return true;
+    *fused_out = t->fused;
+    return t->layers;
+}
+
+void forget_layer_tables() {
+    std::lock_guard<std::mutex> lk(g_tables_mu);
+    g_tables_n = 0;
 }
 
 }  // namespace q35
+
+extern "C" void qwen35_b200_forget_tables(void) { q35::forget_layer_tables(); }
 
 extern "C" int qwen35_b200_prefill_bf16(const Qwen35PrefillArgs* in, qwen35_stream_t stream) {
     using namespace q35;
@@ -167,12 +184,12 @@ extern "C" int qwen35_b200_prefill_bf16(const Qwen35PrefillArgs* in, qwen35_stre
         set_error("null tensor pointer");
         return QWEN35_ERR_BAD_ARG;
     }
-    HostTables tables;
-    const HostTables* t = &tables;
-    if (!read_tables(&tables, in->layer_weights, in->fused_layer_weights, (cudaStream_t)stream)) return QWEN35_ERR_CUDA;
+    const void* fused_h = nullptr;
+    const void* layers_h = host_layer_tables(in->layer_weights, in->fused_layer_weights, &fused_h);
+    if (!layers_h) return QWEN35_ERR_CUDA;
     PrefillArgs a = {};
     a.token_ids = in->token_ids; a.S = in->seq_len; a.out_token = in->out_token;
-    a.embed = (const bf16*)in->embed_weight; a.layers_host = t->layers; a.fused_host = t->fused;
+    a.embed = (const bf16*)in->embed_weight; a.layers_host = (const LayerRec*)layers_h; a.fused_host = (const PrefillFused*)fused_h;
     a.final_norm = (const bf16*)in->final_norm_weight; a.lm_head = (const bf16*)in->lm_head_weight;
     a.k_cache = (bf16*)in->fa_k_cache; a.v_cache = (bf16*)in->fa_v_cache; a.dn_states = (float*)in->dn_states; a.conv_bufs = (float*)in->conv_bufs;
     a.hidden = (bf16*)in->hidden; a.residual = (bf16*)in->residual; a.normalized = (bf16*)in->normalized;

@@ -76,6 +76,7 @@ SIGNATURES = {
     "launch_quantize_nvfp4_out": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp]),
     "launch_quantize_nvfp4_lm_out": (_i, [_vp, _i, _i, _vp, _vp, _vp]),
     "qwen35_b200_decode_batched": (_i, [C.POINTER(BatchedArgs), _vp]),
+    "qwen35_b200_forget_tables": (None, []),
     "qwen35_b200_gemm_bf16": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "qwen35_b200_status": (_i, [_vp]),
     "qwen35_b200_clear_status": (_i, [_vp]),

@@ -182,6 +182,7 @@ def _attach_prefill_fused_weights(weights):
 
 def _pack_prefill_fused_layer_weights(fused_layer_data, device="cuda"):
     """Device blob of 6-pointer records (reference model.py:450-470); the four NVFP4 slots stay null."""
+    _capi.lib().qwen35_b200_forget_tables()       # a new table may reuse the address of a freed one
     buf = bytearray(len(fused_layer_data) * 48)
     for i, ld in enumerate(fused_layer_data):
         struct.pack_into("QQQQQQ", buf, i * 48, ld["proj_weight"].data_ptr(), ld["gate_up_weight"].data_ptr(), 0, 0, 0, 0)
