@@ -122,6 +122,33 @@ def prefill_flops(S: int) -> float:
     return S * (2 * 498_113_344 + 24_576 * S + 47.2e6) + 2 * 254_279_680
 
 
+def prefill_sweep(weights_gpu, dev, lengths):
+    """batched prefill at each prompt length (ids seed 7+S): 3 warm-up runs, 5 timed with CUDA
+    events, best time reported with its share of the measured dense bf16 peak."""
+    from qwen35_b200.config import QWEN35_0P8B as D
+    from qwen35_b200.model import Decoder
+    from qwen35_b200.weights import make_token_ids
+    dec = Decoder(weights=weights_gpu, max_seq_len=max(lengths), device=dev)
+    out = []
+    for S in lengths:
+        ids = make_token_ids(S, 7 + S, D.vocab).to(dev)
+        times = []
+        for i in range(8):
+            dec.reset()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            dec.prefill_tokens(ids)
+            e1.record()
+            torch.cuda.synchronize(dev)
+            if i >= 3:
+                times.append(e0.elapsed_time(e1))
+        dec.check_status()
+        ms = min(times)
+        tf = prefill_flops(S) / (ms * 1e-3) / 1e12
+        out.append({"S": S, "ms": ms, "tok_s": S / (ms * 1e-3), "tflops": tf, "tensor_frac": tf / measured_tensor_peak()})
+    return out
+
+
 def batched_decode_bench(weights_gpu, dev, rank, n_seq, ctx, n_steps):
     """`n_seq` independent sequences per GPU, `ctx`-token contexts prefilled by the library's own
     prefill, `n_steps` greedy steps.  Returns (tok/s on this rank, ms per step, algorithmic bytes per step)."""
@@ -311,6 +338,9 @@ def run_ours(args):
     clocks = sampler.stop()
     dec.check_status()
 
+    sweep = None
+    if args.prefill_sweep and rank == 0:
+        sweep = prefill_sweep(wg, dev, [int(x) for x in args.prefill_sweep.split(",")])
     batched = None
     if args.batched > 0:
         b_tok_s, b_ms, b_bytes = batched_decode_bench(wg, dev, rank, args.batched, args.batched_ctx, GEN)
@@ -369,6 +399,8 @@ def run_ours(args):
         }
         if batched:
             line["batched_decode"] = batched
+        if sweep:
+            line["prefill_sweep"] = sweep
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(w_cpu, ids_cpu, 16, use_hf=False)
         print(json.dumps(line))

@@ -216,6 +216,76 @@ typedef struct {
 } Qwen35BatchedArgs;
 int qwen35_b200_decode_batched(const Qwen35BatchedArgs* args, qwen35_stream_t stream);
 
+/* ---- Tree verification for the 27B-class target (additive: the reference runs this pass as a ggml graph,
+ * models/qwen35_27b/src/qwen35_target_graph.cpp:281-804, with the tree logic in models/qwen35_27b/test/test_dflash.cpp).
+ * One call evaluates the n_nodes nodes of a draft tree (DFS order, node 0 = root, parents[t] < t, -1 for the root)
+ * on top of `past` committed tokens; a node's result is that of the sequential model on its root-to-node path.
+ * Layer il is full attention when il % fa_period == fa_period - 1, else DeltaNet.  head_dim must be 256 and the
+ * DeltaNet head size 128; hidden and ffn multiples of 256; n_nodes <= 40. */
+typedef struct {
+    int n_layers, hidden, ffn, vocab;
+    int q_heads, kv_heads, head_dim;
+    int dn_k_heads, dn_v_heads, dn_dim;
+    int rot_dim, fa_period;
+    float rope_theta, rms_eps;
+} Qwen35TreeDims;
+
+/* Weights of one layer.  Q4_K matrices are row-major arrays of 144-byte super-blocks (256 weights each), rows of the
+ * fused matrices concatenated (a GGUF loader concatenates the tensors' bytes: attn_q|attn_k|attn_v, attn_qkv|attn_gate,
+ * ffn_gate|ffn_up; tensor names src/gguf_target_loader.cpp:7-39).  Norm and SSM vectors are f32 as in GGUF. */
+typedef struct {
+    const void* attn_norm;   /* f32 [hidden], applied as a plain multiply */
+    const void* post_norm;   /* f32 [hidden] */
+    const void* w_in;        /* Q4_K; FA: [2*q_heads*256 + 2*kv_heads*256, hidden], rows [per head q|gate][k][v]; DN: [conv_ch + v_heads*128, hidden], rows [q k v][z] */
+    const void* w_ba;        /* DN: bf16 [2*v_heads, hidden], rows [beta ; alpha] */
+    const void* w_out;       /* Q4_K [hidden, q_heads*256] or [hidden, v_heads*128] */
+    const void* w_gate_up;   /* Q4_K [2*ffn, hidden], rows [gate ; up] */
+    const void* w_down;      /* Q4_K [hidden, ffn] */
+    const void* q_norm;      /* FA: f32 [256] */
+    const void* k_norm;      /* FA: f32 [256] */
+    const void* conv_w;      /* DN: f32 [conv_ch][4], tap 3 multiplies the current input */
+    const void* ssm_a;       /* DN: f32 [v_heads], -exp(A_log) */
+    const void* dt_bias;     /* DN: f32 [v_heads] */
+    const void* ssm_norm;    /* DN: f32 [128] */
+    const void* reserved[3];
+} Qwen35TreeLayer;
+
+typedef struct {
+    Qwen35TreeDims dims;
+    const Qwen35TreeLayer* layers;   /* HOST array [n_layers] of device pointers */
+    const void* token_embd;          /* Q4_K [vocab, hidden] */
+    const void* output_norm;         /* f32 [hidden] */
+    const void* output_w;            /* Q4_K [vocab, hidden] */
+    int n_nodes; int max_nodes;      /* nodes in this tree; node capacity of node_states / node_conv */
+    const int* node_tokens;          /* device int32 [n_nodes] */
+    const int* parents;              /* device int32 [n_nodes] */
+    int past; int max_ctx;           /* committed tokens; cache capacity (past + n_nodes <= max_ctx) */
+    void* k_cache; void* v_cache;    /* bf16 [n_fa][kv_heads][max_ctx][256]; node t is written at slot past + t */
+    void* ssm_state;                 /* f32 [n_dn][v_heads][128 value][128 key] */
+    void* conv_state;                /* f32 [n_dn][3][conv_ch], row 2 newest */
+    void* node_states;               /* f16 [n_dn][max_nodes][v_heads][128][128]: every node's post-state */
+    void* node_conv;                 /* f32 [n_dn][max_nodes][conv_ch]: every node's conv input row */
+    int* node_argmax;                /* device int32 [n_nodes] out */
+    void* logits_out;                /* optional bf16 [n_nodes][vocab] */
+    void* dbg_hidden;                /* optional bf16 [n_layers][n_nodes][hidden] */
+    int dbg_num_layers;              /* > 0: stop after this many layers (the head still runs) */
+    void* scratch; size_t scratch_bytes;   /* caller-owned, >= qwen35_b200_tree_scratch_bytes() */
+    const void* dbg_teacher;         /* optional bf16 [n_layers][n_nodes][hidden]: layer l > 0 reads row block l as its input */
+} Qwen35TreeVerifyArgs;
+
+size_t qwen35_b200_tree_scratch_bytes(const Qwen35TreeDims* dims, int n_nodes, int max_ctx);
+int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* args, qwen35_stream_t stream);
+/* follow_verified_tree (test_dflash.cpp:396-415) on the device: path[i] = DFS index of the i-th accepted node
+ * (path[0] = 0), result[0] = accepted length, result[1] = the next token (arg-max of the last accepted node). */
+int qwen35_b200_tree_accept(const int* node_tokens, const int* parents, const int* node_argmax, int n_nodes, int* path, int* result,
+                            qwen35_stream_t stream);
+/* The commit of test_dflash.cpp:1355-1521, reading path / result from device memory (no host round trip): recurrent
+ * state <- persisted f16 state of the last accepted node, conv state <- the last three inputs along the accepted
+ * chain, K/V rows of the accepted nodes compacted to slots past, past+1, ...  The caller then adds result[0] to past. */
+int qwen35_b200_tree_commit(const Qwen35TreeVerifyArgs* args, const int* path, const int* result, qwen35_stream_t stream);
+/* Q4_K super-blocks -> f32 (bit-exact with the published dequantisation (d*sc)*q - dmin*m) and / or bf16. */
+int qwen35_b200_dequant_q4k(const void* blocks, size_t n_blocks, void* out_f32, void* out_bf16, qwen35_stream_t stream);
+
 /* The prefill and batched-decode entry points keep a host copy of the device pointer tables, keyed by the two
  * table addresses, exactly as the reference keeps its host copy (prefill.cu:1179-1195): after the first call they
  * neither synchronise nor allocate.  A caller that frees its tables and packs new ones may get the same addresses

@@ -1,0 +1,774 @@
+// Tree verification for the 27B-class hybrid target: one forward pass over the N nodes of a draft tree (DFS order,
+// node 0 = root) on top of a committed context, then the accepted-path walk and the commit of that path's state.
+// Replaces the ggml graph of the reference's target (models/qwen35_27b/src/qwen35_target_graph.cpp:281-804) and the
+// host-side tree code around it (models/qwen35_27b/test/test_dflash.cpp:396-442, 1355-1521).
+//
+// A node's result is that of the sequential model run on its root-to-node token path:
+//   full attention   K/V of node t go to cache slot past + t; node t sees slots < past and its ancestors-or-self
+//                    (a 64-bit ancestor word per node is the tree mask); position = past + depth(t)
+//   DeltaNet         the short conv gathers each node's three predecessors along its parent chain (then the
+//                    committed conv state); the recurrence runs in DFS order, reloads the parent's state when the
+//                    DFS order branches, and persists every node's post-state as f16 for the commit
+// Weights are Q4_K super-blocks (256 weights in 144 bytes).  A linear layer dequantises a row panel of the matrix
+// to bf16 into a scratch panel that stays in L2 (HBM sees the 4.5-bit weights once) and runs the tcgen05 split-K
+// GEMM on the panel; the attention products run on mma.sync tiles with K/V staged through shared memory.
+// Dimensions are run-time values (head_dim 256 and DeltaNet head size 128 are fixed).
+#include <cuda_fp16.h>
+
+#include <cmath>
+
+#include "common.cuh"
+#include "runtime.h"
+
+namespace q35 {
+
+int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ldc, const bf16* R, int ldr,
+              int M, int N, int K, int epi, int up_row_offset, cudaStream_t stream);
+
+constexpr int TV_MAX_NODES = 40;       // query rows of one kv head (nodes x q-per-kv) must fit shared memory
+constexpr int TV_HD = 256;             // attention head size
+constexpr int TV_DN = 128;             // DeltaNet head size
+constexpr int TV_CHUNK = 128;          // keys per attention CTA
+constexpr int TV_QSTRIDE = TV_HD + 8;  // padded shared-memory row (bf16 elements): conflict-free fragment loads
+constexpr int TV_PSTRIDE = TV_CHUNK + 8;
+constexpr size_t TV_PANEL_BYTES = 48u << 20;   // dequantised bf16 panel, sized to stay in the 126 MB L2
+
+struct TvDims {
+    int n_layers, hidden, ffn, vocab, q_heads, kv_heads, head_dim, dn_k_heads, dn_v_heads, dn_dim, rot_dim, fa_period;
+    float theta, eps;
+};
+
+// ------------------------------------------------ Q4_K ------------------------------------------------
+// super-block: f16 d, f16 dmin, 12 bytes of 6-bit scales and mins for 8 sub-blocks of 32, 128 bytes of nibbles.
+// value = (d * sc) * q - (dmin * m), every operation a separate f32 rounding (the published dequantisation).
+__device__ __forceinline__ void q4k_scale_min(const uint8_t* s, int j, int& sc, int& m) {
+    if (j < 4) { sc = s[j] & 63; m = s[j + 4] & 63; }
+    else { sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4); m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4); }
+}
+
+// one warp per super-block; lane l owns nibble bytes [4l, 4l+4): 4 low-nibble and 4 high-nibble weights
+__device__ __forceinline__ void q4k_dequant_lane(const uint8_t* blk, int lane, float (&lo)[4], float (&hi)[4], int& e_lo) {
+    const float d = __half2float(*reinterpret_cast<const __half*>(blk));
+    const float dmin = __half2float(*reinterpret_cast<const __half*>(blk + 2));
+    const int g = lane >> 3, pos = (lane & 7) * 4;
+    int sc0, m0, sc1, m1;
+    q4k_scale_min(blk + 4, 2 * g, sc0, m0);
+    q4k_scale_min(blk + 4, 2 * g + 1, sc1, m1);
+    const float d0 = __fmul_rn(d, (float)sc0), mm0 = __fmul_rn(dmin, (float)m0);
+    const float d1 = __fmul_rn(d, (float)sc1), mm1 = __fmul_rn(dmin, (float)m1);
+    const uint32_t qb = *reinterpret_cast<const uint32_t*>(blk + 16 + lane * 4);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t b = (qb >> (8 * i)) & 0xFF;
+        lo[i] = __fsub_rn(__fmul_rn(d0, (float)(b & 0xF)), mm0);
+        hi[i] = __fsub_rn(__fmul_rn(d1, (float)(b >> 4)), mm1);
+    }
+    e_lo = g * 64 + pos;          // low-nibble weights at e_lo.., high-nibble weights at e_lo + 32..
+}
+
+// rows [row0, row0+rows) of a [*, cols] matrix -> bf16 panel (and / or f32 copy)
+__global__ void __launch_bounds__(256) tv_dequant_q4k_kernel(const uint8_t* __restrict__ blocks, size_t first_block, size_t n_blocks,
+                                                             bf16* __restrict__ out_bf16, float* __restrict__ out_f32) {
+    const size_t b = (size_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (b >= n_blocks) return;
+    const int lane = threadIdx.x & 31;
+    float lo[4], hi[4];
+    int e;
+    q4k_dequant_lane(blocks + (first_block + b) * 144, lane, lo, hi, e);
+    if (out_bf16) {
+        bf16* o = out_bf16 + b * 256 + e;
+        const __nv_bfloat162 l0 = __halves2bfloat162(f2bf(lo[0]), f2bf(lo[1])), l1 = __halves2bfloat162(f2bf(lo[2]), f2bf(lo[3]));
+        const __nv_bfloat162 h0 = __halves2bfloat162(f2bf(hi[0]), f2bf(hi[1])), h1 = __halves2bfloat162(f2bf(hi[2]), f2bf(hi[3]));
+        *reinterpret_cast<uint2*>(o) = make_uint2(*reinterpret_cast<const uint32_t*>(&l0), *reinterpret_cast<const uint32_t*>(&l1));
+        *reinterpret_cast<uint2*>(o + 32) = make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+    }
+    if (out_f32) {
+        float* o = out_f32 + b * 256 + e;
+        *reinterpret_cast<float4*>(o) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+        *reinterpret_cast<float4*>(o + 32) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+    }
+}
+
+// embedding rows of the node tokens, bf16
+__global__ void __launch_bounds__(32) tv_embed_q4k_kernel(const uint8_t* __restrict__ embd, const int* __restrict__ tokens, int hidden,
+                                                          bf16* __restrict__ out) {
+    const int t = blockIdx.x, blk = blockIdx.y, lane = threadIdx.x;
+    const size_t b = (size_t)tokens[t] * (hidden / 256) + blk;
+    float lo[4], hi[4];
+    int e;
+    q4k_dequant_lane(embd + b * 144, lane, lo, hi, e);
+    bf16* o = out + (size_t)t * hidden + blk * 256 + e;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { o[i] = f2bf(lo[i]); o[32 + i] = f2bf(hi[i]); }
+}
+
+// ------------------------------------------- tree bookkeeping -------------------------------------------
+// depth[t] and the ancestor-or-self word anc[t] (bit j set: node j is on the root-to-t path); parents[t] < t.
+__global__ void tv_tree_prep_kernel(const int* __restrict__ parents, int n, int* __restrict__ depth, unsigned long long* __restrict__ anc) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    for (int t = 0; t < n; ++t) {
+        const int p = parents[t];
+        const bool ok = p >= 0 && p < t;
+        depth[t] = ok ? depth[p] + 1 : 0;
+        anc[t] = (ok ? anc[p] : 0ull) | (1ull << t);
+    }
+}
+
+// ---------------------------------------------- norms ----------------------------------------------
+__device__ __forceinline__ float tv_block_sum(float v, float* red) {
+    v = warp_sum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < nw; ++i) t += red[i];
+    return t;
+}
+
+// y = bf16(x * rsqrt(mean x^2 + eps) * w), w f32 applied as a plain multiply (qwen35_target_graph.cpp:260-264)
+__global__ void __launch_bounds__(256) tv_rmsnorm_kernel(const bf16* __restrict__ x, const float* __restrict__ w, bf16* __restrict__ out, int H, float eps) {
+    __shared__ float red[8];
+    const bf16* xr = x + (size_t)blockIdx.x * H;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < H; i += 256) { const float v = bf2f(xr[i]); ss = fmaf(v, v, ss); }
+    const float inv = rsqrt_ieee(tv_block_sum(ss, red) / (float)H + eps);
+    for (int i = threadIdx.x; i < H; i += 256) out[(size_t)blockIdx.x * H + i] = f2bf(bf2f(xr[i]) * inv * w[i]);
+}
+
+// ------------------------------------------ full attention ------------------------------------------
+// one CTA (128 threads, 2 elements each) per (node, slot): q heads, then k heads, then v heads of the projection row
+// [per q head: q(256) | gate(256)] [k heads] [v heads].  Head RMSNorm (plain weight), rotate-half RoPE over rot_dim.
+__global__ void __launch_bounds__(128) tv_fa_prep_kernel(const bf16* __restrict__ proj, int ldp, const float* __restrict__ qn, const float* __restrict__ kn,
+                                                         const int* __restrict__ depth, TvDims D, int past, int max_ctx,
+                                                         bf16* __restrict__ qbuf, bf16* __restrict__ k_cache, bf16* __restrict__ v_cache) {
+    __shared__ float red[4];
+    __shared__ float xs[TV_HD];
+    const int t = blockIdx.x, slot = blockIdx.y, tid = threadIdx.x;
+    const bf16* row = proj + (size_t)t * ldp;
+    const int qcols = 2 * D.q_heads * TV_HD;
+    if (slot >= D.q_heads + D.kv_heads) {                      // v head: copy into the cache slot
+        const int kvh = slot - D.q_heads - D.kv_heads;
+        const bf16* src = row + qcols + (D.kv_heads + kvh) * TV_HD;
+        bf16* dst = v_cache + ((size_t)kvh * max_ctx + past + t) * TV_HD;
+        dst[tid] = src[tid]; dst[tid + 128] = src[tid + 128];
+        return;
+    }
+    const bool isq = slot < D.q_heads;
+    const bf16* src = isq ? row + (size_t)slot * 2 * TV_HD : row + qcols + (slot - D.q_heads) * TV_HD;
+    const float* w = isq ? qn : kn;
+    const float a = bf2f(src[tid]), b = bf2f(src[tid + 128]);
+    const float inv = rsqrt_ieee(tv_block_sum(fmaf(a, a, b * b), red) / (float)TV_HD + D.eps);
+    xs[tid] = a * inv * w[tid];
+    xs[tid + 128] = b * inv * w[tid + 128];
+    __syncthreads();
+    const float pos = (float)(past + depth[t]);
+    const int half = D.rot_dim / 2;
+    float y[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int e = tid + 128 * k;
+        float v = xs[e];
+        if (e < D.rot_dim) {
+            const int i = e < half ? e : e - half;
+            const float inv_freq = powf(D.theta, -(float)(2 * i) / (float)D.rot_dim);
+            float sn, cs;
+            sincosf(pos * inv_freq, &sn, &cs);
+            v = e < half ? xs[e] * cs - xs[e + half] * sn : xs[e] * cs + xs[e - half] * sn;
+        }
+        y[k] = v;
+    }
+    bf16* dst = isq ? qbuf + ((size_t)t * D.q_heads + slot) * TV_HD
+                    : k_cache + ((size_t)(slot - D.q_heads) * max_ctx + past + t) * TV_HD;
+    dst[tid] = f2bf(y[0]); dst[tid + 128] = f2bf(y[1]);
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// scores of all query rows of one kv head (row r = node * gqa + q-in-group) against one chunk of keys:
+// s = (q . k) / 16 in f32, masked to -inf outside [0, past) and the node's ancestors.  grid (chunks, kv_heads).
+__global__ void __launch_bounds__(256, 1) tv_att_scores_kernel(const bf16* __restrict__ qbuf, const bf16* __restrict__ k_cache,
+                                                               const unsigned long long* __restrict__ anc, TvDims D, int n_nodes, int past,
+                                                               int max_ctx, int lpad, float* __restrict__ scores) {
+    extern __shared__ __align__(16) unsigned char tv_smem[];
+    bf16* Qs = reinterpret_cast<bf16*>(tv_smem);
+    const int gqa = D.q_heads / D.kv_heads, R = n_nodes * gqa, mt_n = (R + 15) / 16;
+    bf16* Ks = Qs + (size_t)mt_n * 16 * TV_QSTRIDE;
+    const int chunk = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int j0 = chunk * TV_CHUNK, L = past + n_nodes;
+    for (int i = tid; i < mt_n * 16 * (TV_HD / 8); i += 256) {
+        const int r = i / (TV_HD / 8), c8 = i % (TV_HD / 8);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r < R) v = *reinterpret_cast<const uint4*>(qbuf + ((size_t)(r / gqa) * D.q_heads + kvh * gqa + r % gqa) * TV_HD + c8 * 8);
+        *reinterpret_cast<uint4*>(Qs + (size_t)r * TV_QSTRIDE + c8 * 8) = v;
+    }
+    for (int i = tid; i < TV_CHUNK * (TV_HD / 8); i += 256) {
+        const int k = i / (TV_HD / 8), c8 = i % (TV_HD / 8);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (j0 + k < L) v = *reinterpret_cast<const uint4*>(k_cache + ((size_t)kvh * max_ctx + j0 + k) * TV_HD + c8 * 8);
+        *reinterpret_cast<uint4*>(Ks + (size_t)k * TV_QSTRIDE + c8 * 8) = v;
+    }
+    __syncthreads();
+    const int g = lane >> 2, c = lane & 3;
+    for (int nt = warp; nt < TV_CHUNK / 8; nt += 8) {
+        uint32_t bfr[TV_HD / 16][2];
+        const bf16* kr = Ks + (size_t)(nt * 8 + g) * TV_QSTRIDE + 2 * c;
+#pragma unroll
+        for (int s = 0; s < TV_HD / 16; ++s) {
+            bfr[s][0] = *reinterpret_cast<const uint32_t*>(kr + s * 16);
+            bfr[s][1] = *reinterpret_cast<const uint32_t*>(kr + s * 16 + 8);
+        }
+        for (int mt = 0; mt < mt_n; ++mt) {
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            const bf16* q0 = Qs + (size_t)(mt * 16 + g) * TV_QSTRIDE + 2 * c;
+            const bf16* q1 = q0 + 8 * TV_QSTRIDE;
+#pragma unroll
+            for (int s = 0; s < TV_HD / 16; ++s) {
+                uint32_t a[4];
+                a[0] = *reinterpret_cast<const uint32_t*>(q0 + s * 16);
+                a[1] = *reinterpret_cast<const uint32_t*>(q1 + s * 16);
+                a[2] = *reinterpret_cast<const uint32_t*>(q0 + s * 16 + 8);
+                a[3] = *reinterpret_cast<const uint32_t*>(q1 + s * 16 + 8);
+                mma_bf16_16816(acc, a, bfr[s][0], bfr[s][1]);
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int r = mt * 16 + g + 8 * h;
+                if (r >= R) continue;
+                const unsigned long long am = anc[r / gqa];
+                float* dst = scores + ((size_t)kvh * R + r) * lpad + j0 + nt * 8 + 2 * c;
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const int j = j0 + nt * 8 + 2 * c + e;
+                    const bool vis = j < past || (j < L && ((am >> (j - past)) & 1ull));
+                    dst[e] = vis ? acc[2 * h + e] * 0.0625f : -INFINITY;
+                }
+            }
+        }
+    }
+}
+
+// softmax statistics of every query row over the whole (masked) key range: one warp per row
+__global__ void __launch_bounds__(256) tv_att_stats_kernel(const float* __restrict__ scores, int rows, int lpad, int len, float* __restrict__ stats) {
+    const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const float* s = scores + (size_t)r * lpad;
+    float mx = -INFINITY;
+    for (int j = lane; j < len; j += 32) mx = fmaxf(mx, s[j]);
+    mx = warp_max(mx);
+    float sm = 0.f;
+    for (int j = lane; j < len; j += 32) sm += expf(s[j] - mx);
+    sm = warp_sum(sm);
+    if (lane == 0) { stats[2 * r] = mx; stats[2 * r + 1] = sm; }
+}
+
+// partial P.V of one chunk of keys for all query rows of one kv head; P = bf16(exp(s - m) / l).  grid (chunks, kv_heads)
+__global__ void __launch_bounds__(256, 1) tv_att_pv_kernel(const bf16* __restrict__ v_cache, const float* __restrict__ scores, const float* __restrict__ stats,
+                                                           TvDims D, int n_nodes, int past, int max_ctx, int lpad, float* __restrict__ partial) {
+    extern __shared__ __align__(16) unsigned char tv_smem[];
+    bf16* Vt = reinterpret_cast<bf16*>(tv_smem);                     // [256 dims][TV_PSTRIDE keys]
+    bf16* Ps = Vt + (size_t)TV_HD * TV_PSTRIDE;                      // [rows][TV_PSTRIDE keys]
+    const int gqa = D.q_heads / D.kv_heads, R = n_nodes * gqa, mt_n = (R + 15) / 16;
+    const int chunk = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int j0 = chunk * TV_CHUNK, L = past + n_nodes;
+    // V chunk transposed: lane <-> key, 8 dims at a time
+    for (int i = tid; i < TV_CHUNK * (TV_HD / 8); i += 256) {
+        const int k = i % TV_CHUNK, c8 = i / TV_CHUNK;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (j0 + k < L) v = *reinterpret_cast<const uint4*>(v_cache + ((size_t)kvh * max_ctx + j0 + k) * TV_HD + c8 * 8);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            Vt[(size_t)(c8 * 8 + 2 * e) * TV_PSTRIDE + k] = __ushort_as_bfloat16((unsigned short)(w[e] & 0xFFFF));
+            Vt[(size_t)(c8 * 8 + 2 * e + 1) * TV_PSTRIDE + k] = __ushort_as_bfloat16((unsigned short)(w[e] >> 16));
+        }
+    }
+    for (int i = tid; i < mt_n * 16 * TV_CHUNK; i += 256) {
+        const int r = i / TV_CHUNK, k = i % TV_CHUNK;
+        float p = 0.f;
+        if (r < R) {
+            const size_t gr = (size_t)kvh * R + r;
+            const float s = scores[gr * lpad + j0 + k];
+            p = (s == -INFINITY) ? 0.f : expf(s - stats[2 * gr]) / stats[2 * gr + 1];
+        }
+        Ps[(size_t)r * TV_PSTRIDE + k] = f2bf(p);
+    }
+    __syncthreads();
+    const int g = lane >> 2, c = lane & 3;
+    const int n_chunks = gridDim.x;
+    for (int nt = warp; nt < TV_HD / 8; nt += 8) {
+        uint32_t bfr[TV_CHUNK / 16][2];
+        const bf16* vr = Vt + (size_t)(nt * 8 + g) * TV_PSTRIDE + 2 * c;
+#pragma unroll
+        for (int s = 0; s < TV_CHUNK / 16; ++s) {
+            bfr[s][0] = *reinterpret_cast<const uint32_t*>(vr + s * 16);
+            bfr[s][1] = *reinterpret_cast<const uint32_t*>(vr + s * 16 + 8);
+        }
+        for (int mt = 0; mt < mt_n; ++mt) {
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            const bf16* p0 = Ps + (size_t)(mt * 16 + g) * TV_PSTRIDE + 2 * c;
+            const bf16* p1 = p0 + 8 * TV_PSTRIDE;
+#pragma unroll
+            for (int s = 0; s < TV_CHUNK / 16; ++s) {
+                uint32_t a[4];
+                a[0] = *reinterpret_cast<const uint32_t*>(p0 + s * 16);
+                a[1] = *reinterpret_cast<const uint32_t*>(p1 + s * 16);
+                a[2] = *reinterpret_cast<const uint32_t*>(p0 + s * 16 + 8);
+                a[3] = *reinterpret_cast<const uint32_t*>(p1 + s * 16 + 8);
+                mma_bf16_16816(acc, a, bfr[s][0], bfr[s][1]);
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int r = mt * 16 + g + 8 * h;
+                if (r < R)
+                    *reinterpret_cast<float2*>(partial + (((size_t)kvh * R + r) * n_chunks + chunk) * TV_HD + nt * 8 + 2 * c) = make_float2(acc[2 * h], acc[2 * h + 1]);
+            }
+        }
+    }
+}
+
+// sum of the chunk partials in chunk order, times sigmoid(gate), one rounding to bf16.  grid (nodes, q_heads), 128 threads
+__global__ void __launch_bounds__(128) tv_att_merge_kernel(const float* __restrict__ partial, const bf16* __restrict__ proj, int ldp, TvDims D,
+                                                           int n_nodes, int n_chunks, bf16* __restrict__ out) {
+    const int t = blockIdx.x, hq = blockIdx.y, tid = threadIdx.x;
+    const int gqa = D.q_heads / D.kv_heads, R = n_nodes * gqa, kvh = hq / gqa, r = t * gqa + hq % gqa;
+    const float* pb = partial + ((size_t)kvh * R + r) * n_chunks * TV_HD;
+    float a0 = 0.f, a1 = 0.f;
+    for (int ch = 0; ch < n_chunks; ++ch) {
+        const float2 v = *reinterpret_cast<const float2*>(pb + (size_t)ch * TV_HD + 2 * tid);
+        a0 += v.x; a1 += v.y;
+    }
+    const bf16* gate = proj + (size_t)t * ldp + (size_t)hq * 2 * TV_HD + TV_HD + 2 * tid;
+    bf16* o = out + ((size_t)t * D.q_heads + hq) * TV_HD + 2 * tid;
+    o[0] = f2bf(a0 * sigmoid_f(bf2f(gate[0])));
+    o[1] = f2bf(a1 * sigmoid_f(bf2f(gate[1])));
+}
+
+// --------------------------------------------- DeltaNet ---------------------------------------------
+// tree short-conv + SiLU: taps of node t = its three predecessors on the parent chain, continuing into the committed
+// conv state [3][channels] (row 2 newest) when the chain ends (qwen35_target_graph.cpp:462-496).  Also keeps the raw
+// projection row of every node for the commit.
+__global__ void __launch_bounds__(256) tv_dn_conv_kernel(const bf16* __restrict__ proj, int ldp, const int* __restrict__ parents,
+                                                         const float* __restrict__ conv_state, const float* __restrict__ conv_w, int conv_ch,
+                                                         float* __restrict__ qkv, float* __restrict__ node_conv) {
+    const int t = blockIdx.x, ch = blockIdx.y * 256 + threadIdx.x;
+    if (ch >= conv_ch) return;
+    float x[4];
+    x[3] = bf2f(proj[(size_t)t * ldp + ch]);
+    node_conv[(size_t)t * conv_ch + ch] = x[3];
+    int a = t, cs = 2;
+#pragma unroll
+    for (int k = 2; k >= 0; --k) {
+        if (a >= 0) a = parents[a];
+        x[k] = (a >= 0) ? bf2f(proj[(size_t)a * ldp + ch]) : conv_state[(size_t)(cs--) * conv_ch + ch];
+    }
+    const float4 w = *reinterpret_cast<const float4*>(conv_w + (size_t)ch * 4);
+    float s = w.x * x[0];
+    s = fmaf(w.y, x[1], s); s = fmaf(w.z, x[2], s); s = fmaf(w.w, x[3], s);
+    qkv[(size_t)t * conv_ch + ch] = silu_f(s);
+}
+
+// L2 norm of the q and k heads (q also scaled by 1/sqrt(128)), and per (node, v head): beta = sigmoid(b),
+// decay = exp(softplus(a + dt_bias) * ssm_a).  grid (nodes, k_heads), 128 threads
+__global__ void __launch_bounds__(128) tv_dn_norm_kernel(float* __restrict__ qkv, int conv_ch, const bf16* __restrict__ ba, int ldba,
+                                                         const float* __restrict__ ssm_a, const float* __restrict__ dt_bias, TvDims D,
+                                                         float* __restrict__ gate /* [nodes][v_heads][2] */) {
+    __shared__ float red[4];
+    const int t = blockIdx.x, kh = blockIdx.y, tid = threadIdx.x;
+    float* q = qkv + (size_t)t * conv_ch + kh * TV_DN;
+    float* k = q + D.dn_k_heads * TV_DN;
+    const float qv = q[tid], kv = k[tid];
+    const float qs = tv_block_sum(qv * qv, red);
+    const float ks = tv_block_sum(kv * kv, red);
+    q[tid] = qv * rsqrt_ieee(qs + D.eps) * 0.08838834764831845f;
+    k[tid] = kv * rsqrt_ieee(ks + D.eps);
+    for (int h = kh * 128 + tid; h < D.dn_v_heads; h += D.dn_k_heads * 128) {
+        const float b = bf2f(ba[(size_t)t * ldba + h]);
+        const float a = bf2f(ba[(size_t)t * ldba + D.dn_v_heads + h]) + dt_bias[h];
+        const float sp = (a > 20.f) ? a : log1pf(expf(a));
+        gate[((size_t)t * D.dn_v_heads + h) * 2] = sigmoid_f(b);
+        gate[((size_t)t * D.dn_v_heads + h) * 2 + 1] = expf(sp * ssm_a[h]);
+    }
+}
+
+// tree gated delta rule: one CTA (4 warps x 4 value rows) per (v head, block of 16 value rows); nodes in DFS order.
+// The running f32 state continues from node t-1 when that is the parent, else it is reloaded from the parent's
+// persisted f16 post-state (or the committed f32 state for a child of nothing).  Every node's post-state is
+// persisted as f16 (qwen35_target_graph.cpp:540-583).  v head h uses k head h % k_heads (ggml_repeat tiling, :531-534).
+__global__ void __launch_bounds__(128) tv_dn_tree_kernel(const float* __restrict__ qkv, int conv_ch, const float* __restrict__ gate,
+                                                         const int* __restrict__ parents, int n_nodes, TvDims D,
+                                                         const float* __restrict__ ssm_state, __half* __restrict__ node_states,
+                                                         float* __restrict__ core) {
+    const int h = blockIdx.x, rb = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kh = h % D.dn_k_heads;
+    const size_t head_elems = (size_t)TV_DN * TV_DN;
+    const int v0 = rb * 16 + warp * 4;
+    float4 st[4];
+    for (int t = 0; t < n_nodes; ++t) {
+        const int p = parents[t];
+        if (t == 0 || p != t - 1) {
+            if (p < 0) {
+#pragma unroll
+                for (int r = 0; r < 4; ++r) st[r] = *(reinterpret_cast<const float4*>(ssm_state + (size_t)h * head_elems + (size_t)(v0 + r) * TV_DN) + lane);
+            } else {
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const uint2 raw = *(reinterpret_cast<const uint2*>(node_states + ((size_t)p * D.dn_v_heads + h) * head_elems + (size_t)(v0 + r) * TV_DN) + lane);
+                    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x)), b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+                    st[r] = make_float4(a.x, a.y, b.x, b.y);
+                }
+            }
+        }
+        const float* row = qkv + (size_t)t * conv_ch;
+        const float4 q4 = *(reinterpret_cast<const float4*>(row + kh * TV_DN) + lane);
+        const float4 k4 = *(reinterpret_cast<const float4*>(row + (D.dn_k_heads + kh) * TV_DN) + lane);
+        const float beta = gate[((size_t)t * D.dn_v_heads + h) * 2], decay = gate[((size_t)t * D.dn_v_heads + h) * 2 + 1];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const float vv = row[2 * D.dn_k_heads * TV_DN + h * TV_DN + v0 + r];
+            float4 u = st[r];
+            u.x = __fmul_rn(u.x, decay); u.y = __fmul_rn(u.y, decay); u.z = __fmul_rn(u.z, decay); u.w = __fmul_rn(u.w, decay);
+            float kv = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(u.x, k4.x), __fmul_rn(u.y, k4.y)), __fmul_rn(u.z, k4.z)), __fmul_rn(u.w, k4.w));
+            kv = warp_sum(kv);
+            const float delta = __fmul_rn(__fsub_rn(vv, kv), beta);
+            u.x = __fadd_rn(u.x, __fmul_rn(k4.x, delta)); u.y = __fadd_rn(u.y, __fmul_rn(k4.y, delta));
+            u.z = __fadd_rn(u.z, __fmul_rn(k4.z, delta)); u.w = __fadd_rn(u.w, __fmul_rn(k4.w, delta));
+            float o = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(u.x, q4.x), __fmul_rn(u.y, q4.y)), __fmul_rn(u.z, q4.z)), __fmul_rn(u.w, q4.w));
+            o = warp_sum(o);
+            st[r] = u;
+            const __half2 h0 = __floats2half2_rn(u.x, u.y), h1 = __floats2half2_rn(u.z, u.w);
+            *(reinterpret_cast<uint2*>(node_states + ((size_t)t * D.dn_v_heads + h) * head_elems + (size_t)(v0 + r) * TV_DN) + lane) =
+                make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+            if (lane == 0) core[((size_t)t * D.dn_v_heads + h) * TV_DN + v0 + r] = o;
+        }
+    }
+}
+
+// gated norm: y = bf16(o * rsqrt(mean o^2 + eps) * w * silu(z)).  grid (nodes, v_heads), 128 threads
+__global__ void __launch_bounds__(128) tv_dn_gated_norm_kernel(const float* __restrict__ core, const bf16* __restrict__ proj, int ldp, int z_off,
+                                                               const float* __restrict__ w, TvDims D, bf16* __restrict__ out) {
+    __shared__ float red[4];
+    const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    const float o = core[((size_t)t * D.dn_v_heads + h) * TV_DN + tid];
+    const float inv = rsqrt_ieee(tv_block_sum(o * o, red) / (float)TV_DN + D.eps);
+    const float z = bf2f(proj[(size_t)t * ldp + z_off + h * TV_DN + tid]);
+    out[((size_t)t * D.dn_v_heads + h) * TV_DN + tid] = f2bf(o * inv * w[tid] * silu_f(z));
+}
+
+// ------------------------------------------- head and walk -------------------------------------------
+// arg-max of every node's bf16 logits, lowest index among equal maxima.  grid nodes, 1024 threads
+__global__ void __launch_bounds__(1024) tv_argmax_kernel(const bf16* __restrict__ logits, int vocab, int* __restrict__ out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const bf16* row = logits + (size_t)blockIdx.x * vocab;
+    float best = -INFINITY; int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < vocab; i += 1024) {
+        const float v = bf2f(row[i]);
+        if (v > best) { best = v; bi = i; }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o); const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = best; si[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        best = sv[threadIdx.x]; bi = si[threadIdx.x];
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o); const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+        }
+        if (threadIdx.x == 0) out[blockIdx.x] = bi;
+    }
+}
+
+// accepted path: from the root follow the child whose token equals the arg-max of the current node
+// (test_dflash.cpp:396-415).  result[0] = path length, result[1] = next token (arg-max of the last accepted node),
+// path[i] = DFS index of the i-th accepted node.
+__global__ void tv_accept_kernel(const int* __restrict__ tokens, const int* __restrict__ parents, const int* __restrict__ argmax, int n,
+                                 int* __restrict__ path, int* __restrict__ result) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    int cur = 0, len = 1;
+    path[0] = 0;
+    for (;;) {
+        const int want = argmax[cur];
+        int next = -1;
+        for (int c = cur + 1; c < n; ++c)
+            if (parents[c] == cur && tokens[c] == want) { next = c; break; }
+        if (next < 0) break;
+        cur = next;
+        path[len++] = cur;
+    }
+    result[0] = len;
+    result[1] = argmax[cur];
+}
+
+// commit (test_dflash.cpp:1355-1521): recurrent state <- persisted state of the last accepted node
+__global__ void tv_commit_state_kernel(const __half* __restrict__ node_states, size_t layer_stride_nodes, size_t node_elems, int n_dn,
+                                       const int* __restrict__ path, const int* __restrict__ result, float* __restrict__ ssm_state) {
+    const int leaf = path[result[0] - 1];
+    const size_t total = (size_t)n_dn * node_elems;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t l = i / node_elems, e = i % node_elems;
+        ssm_state[i] = __half2float(node_states[l * layer_stride_nodes + (size_t)leaf * node_elems + e]);
+    }
+}
+// conv state <- the last three inputs along [old state rows 0..2, accepted nodes...]
+__global__ void tv_commit_conv_kernel(const float* __restrict__ node_conv, size_t layer_stride_nodes, int conv_ch, int n_dn,
+                                      const int* __restrict__ path, const int* __restrict__ result, float* __restrict__ conv_state) {
+    const int len = result[0];
+    const size_t total = (size_t)n_dn * conv_ch;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t l = i / conv_ch, ch = i % conv_ch;
+        float* cs = conv_state + l * 3 * conv_ch;
+        float old[3] = {cs[ch], cs[conv_ch + ch], cs[2 * (size_t)conv_ch + ch]};
+        float nv[3];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            const int idx = len + k;                 // position in [old0, old1, old2, node path...] of new row k
+            nv[k] = idx < 3 ? old[idx] : node_conv[l * layer_stride_nodes + (size_t)path[idx - 3] * conv_ch + ch];
+        }
+        cs[ch] = nv[0]; cs[conv_ch + ch] = nv[1]; cs[2 * (size_t)conv_ch + ch] = nv[2];
+    }
+}
+// K/V rows of the accepted nodes move to slots past, past+1, ... (ascending, so no source is overwritten early)
+__global__ void tv_commit_kv_kernel(bf16* __restrict__ k_cache, bf16* __restrict__ v_cache, size_t layer_stride, int n_fa, int kv_heads, int max_ctx, int past,
+                                    const int* __restrict__ path, const int* __restrict__ result) {
+    const int len = result[0];
+    const int per_row = TV_HD / 8;
+    const size_t total = (size_t)n_fa * kv_heads * per_row * 2;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const int c8 = (int)(i % per_row);
+        const size_t rest = i / per_row;
+        const int which = (int)(rest % 2);
+        const size_t lh = rest / 2;                  // layer * kv_heads + head
+        bf16* base = (which ? v_cache : k_cache) + (lh / kv_heads) * layer_stride + ((lh % kv_heads) * (size_t)max_ctx) * TV_HD + c8 * 8;
+        for (int d = 0; d < len; ++d) {
+            const int src = past + path[d], dst = past + d;
+            if (src != dst) *reinterpret_cast<uint4*>(base + (size_t)dst * TV_HD) = *reinterpret_cast<const uint4*>(base + (size_t)src * TV_HD);
+        }
+    }
+}
+
+// ------------------------------------------------ host ------------------------------------------------
+struct TvScratch {
+    bf16 *hidden, *resid, *normed, *proj, *ba, *qbuf, *attn, *mlp, *panel, *logits;
+    float *dn_qkv, *dn_gate, *core, *scores, *stats, *partial;
+    int* depth; unsigned long long* anc;
+    size_t bytes;
+};
+
+static size_t align_up(size_t v) { return (v + 255) & ~(size_t)255; }
+
+static TvScratch tv_layout(const TvDims& D, int n, int max_ctx, char* base) {
+    TvScratch s;
+    size_t off = 0;
+    auto take = [&](size_t bytes) { char* p = base ? base + off : nullptr; off += align_up(bytes); return p; };
+    const int conv_ch = (2 * D.dn_k_heads + D.dn_v_heads) * TV_DN;
+    const int fa_in = (2 * D.q_heads + 2 * D.kv_heads) * TV_HD, dn_in = conv_ch + D.dn_v_heads * TV_DN;
+    const int proj_w = fa_in > dn_in ? fa_in : dn_in;
+    const int att_w = D.q_heads * TV_HD > D.dn_v_heads * TV_DN ? D.q_heads * TV_HD : D.dn_v_heads * TV_DN;
+    const int lpad = ((max_ctx + TV_CHUNK - 1) / TV_CHUNK) * TV_CHUNK, chunks = lpad / TV_CHUNK;
+    s.hidden = (bf16*)take((size_t)n * D.hidden * 2); s.resid = (bf16*)take((size_t)n * D.hidden * 2); s.normed = (bf16*)take((size_t)n * D.hidden * 2);
+    s.proj = (bf16*)take((size_t)n * proj_w * 2); s.ba = (bf16*)take((size_t)n * 2 * D.dn_v_heads * 2);
+    s.qbuf = (bf16*)take((size_t)n * D.q_heads * TV_HD * 2); s.attn = (bf16*)take((size_t)n * att_w * 2);
+    s.mlp = (bf16*)take((size_t)n * D.ffn * 2); s.panel = (bf16*)take(TV_PANEL_BYTES); s.logits = (bf16*)take((size_t)n * D.vocab * 2);
+    s.dn_qkv = (float*)take((size_t)n * conv_ch * 4); s.dn_gate = (float*)take((size_t)n * D.dn_v_heads * 2 * 4);
+    s.core = (float*)take((size_t)n * D.dn_v_heads * TV_DN * 4);
+    s.scores = (float*)take((size_t)n * D.q_heads * lpad * 4); s.stats = (float*)take((size_t)n * D.q_heads * 2 * 4);
+    s.partial = (float*)take((size_t)n * D.q_heads * chunks * TV_HD * 4);
+    s.depth = (int*)take(64 * 4); s.anc = (unsigned long long*)take(64 * 8);
+    s.bytes = off;
+    return s;
+}
+
+static bool tv_dims_ok(const TvDims& D) {
+    return D.head_dim == TV_HD && D.dn_dim == TV_DN && D.hidden % 256 == 0 && D.ffn % 256 == 0 && D.q_heads % D.kv_heads == 0 &&
+           D.rot_dim % 2 == 0 && D.rot_dim <= TV_HD && D.dn_v_heads % D.dn_k_heads == 0 && D.n_layers > 0 && D.fa_period > 0 && D.vocab > 0;
+}
+
+// C[M, out_rows] = epi(X[M, in] . dequant(W[out_rows, in])^T), panel by panel.  epi 2: W = [gate rows ; up rows], out = ffn
+static int q4k_linear(const bf16* X, int lda, const uint8_t* W, int out_rows, int in_cols, bf16* C, int ldc, const bf16* R, int ldr,
+                      int M, int epi, bf16* panel, cudaStream_t stream) {
+    const size_t bpr = (size_t)in_cols / 256;                               // super-blocks per weight row
+    const int sets = epi == 2 ? 2 : 1;
+    int pr = (int)(TV_PANEL_BYTES / ((size_t)in_cols * 2 * sets));
+    pr = pr >= 128 ? (pr / 128) * 128 : pr;
+    if (pr <= 0) { set_error("tree_verify: a weight row of %d columns does not fit the dequantisation panel", in_cols); return QWEN35_ERR_BAD_ARG; }
+    for (int r0 = 0; r0 < out_rows; r0 += pr) {
+        const int rows = out_rows - r0 < pr ? out_rows - r0 : pr;
+        const size_t nb = (size_t)rows * bpr;
+        tv_dequant_q4k_kernel<<<(unsigned)((nb + 7) / 8), 256, 0, stream>>>(W, (size_t)r0 * bpr, nb, panel, nullptr);
+        if (epi == 2)
+            tv_dequant_q4k_kernel<<<(unsigned)((nb + 7) / 8), 256, 0, stream>>>(W, ((size_t)out_rows + r0) * bpr, nb, panel + (size_t)rows * in_cols, nullptr);
+        g_launches.fetch_add(sets);
+        const int st = gemm_bf16(X, lda, panel, rows * sets, C + r0, ldc, R ? R + r0 : nullptr, ldr, M, rows, in_cols, epi, rows, stream);
+        if (st != QWEN35_OK) return st;
+    }
+    return QWEN35_OK;
+}
+
+}  // namespace q35
+
+#define Q35_TRYT(expr)                       \
+    do {                                     \
+        const int st__ = (expr);             \
+        if (st__ != QWEN35_OK) return st__;  \
+    } while (0)
+
+static q35::TvDims to_dims(const Qwen35TreeDims* d) {
+    q35::TvDims D;
+    D.n_layers = d->n_layers; D.hidden = d->hidden; D.ffn = d->ffn; D.vocab = d->vocab; D.q_heads = d->q_heads; D.kv_heads = d->kv_heads;
+    D.head_dim = d->head_dim; D.dn_k_heads = d->dn_k_heads; D.dn_v_heads = d->dn_v_heads; D.dn_dim = d->dn_dim; D.rot_dim = d->rot_dim;
+    D.fa_period = d->fa_period; D.theta = d->rope_theta; D.eps = d->rms_eps;
+    return D;
+}
+
+extern "C" size_t qwen35_b200_tree_scratch_bytes(const Qwen35TreeDims* dims, int n_nodes, int max_ctx) {
+    if (!dims) return 0;
+    return q35::tv_layout(to_dims(dims), n_nodes, max_ctx, nullptr).bytes;
+}
+
+extern "C" int qwen35_b200_dequant_q4k(const void* blocks, size_t n_blocks, void* out_f32, void* out_bf16, qwen35_stream_t stream) {
+    using namespace q35;
+    if (!blocks || (!out_f32 && !out_bf16)) { set_error("dequant_q4k: null pointer"); return QWEN35_ERR_BAD_ARG; }
+    if (n_blocks == 0) return QWEN35_OK;
+    tv_dequant_q4k_kernel<<<(unsigned)((n_blocks + 7) / 8), 256, 0, (cudaStream_t)stream>>>((const uint8_t*)blocks, 0, n_blocks, (bf16*)out_bf16, (float*)out_f32);
+    Q35_CUDA_OK(cudaGetLastError());
+    g_launches.fetch_add(1);
+    return QWEN35_OK;
+}
+
+extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_stream_t stream_) {
+    using namespace q35;
+    cudaStream_t stream = (cudaStream_t)stream_;
+    if (!in || !in->layers) { set_error("tree_verify: null args"); return QWEN35_ERR_BAD_ARG; }
+    const TvDims D = to_dims(&in->dims);
+    const int n = in->n_nodes;
+    if (!tv_dims_ok(D)) { set_error("tree_verify: unsupported dimensions (head_dim must be 256, DeltaNet head 128, hidden and ffn multiples of 256)"); return QWEN35_ERR_BAD_ARG; }
+    const int gqa = D.q_heads / D.kv_heads;
+    if (n <= 0 || n > TV_MAX_NODES || n * gqa > 240) { set_error("tree_verify: %d nodes out of range (1..%d, nodes x q-per-kv <= 240)", n, TV_MAX_NODES); return QWEN35_ERR_BAD_ARG; }
+    if (in->past < 0 || in->past + n > in->max_ctx) { set_error("tree_verify: past %d + %d nodes exceeds max_ctx %d", in->past, n, in->max_ctx); return QWEN35_ERR_BAD_ARG; }
+    if (!in->token_embd || !in->output_norm || !in->output_w || !in->node_tokens || !in->parents || !in->k_cache || !in->v_cache || !in->ssm_state ||
+        !in->conv_state || !in->node_states || !in->node_conv || !in->node_argmax || !in->scratch) {
+        set_error("tree_verify: null tensor pointer");
+        return QWEN35_ERR_BAD_ARG;
+    }
+    const TvScratch need = tv_layout(D, n, in->max_ctx, nullptr);
+    if (in->scratch_bytes < need.bytes) { set_error("tree_verify: scratch of %zu bytes given, %zu needed", in->scratch_bytes, need.bytes); return QWEN35_ERR_BAD_ARG; }
+    const TvScratch s = tv_layout(D, n, in->max_ctx, (char*)in->scratch);
+    void* ws = get_workspace();
+    if (!ws) return QWEN35_ERR_CUDA;
+
+    const int conv_ch = (2 * D.dn_k_heads + D.dn_v_heads) * TV_DN, z_off = conv_ch;
+    const int fa_in = (2 * D.q_heads + 2 * D.kv_heads) * TV_HD, dn_in = conv_ch + D.dn_v_heads * TV_DN;
+    const int L = in->past + n, lpad = ((in->max_ctx + TV_CHUNK - 1) / TV_CHUNK) * TV_CHUNK;
+    const int chunks = (L + TV_CHUNK - 1) / TV_CHUNK;          // chunks that hold visible keys
+    const int R = n * gqa, mt_n = (R + 15) / 16;
+    const size_t sc_smem = ((size_t)mt_n * 16 * TV_QSTRIDE + (size_t)TV_CHUNK * TV_QSTRIDE) * 2;
+    const size_t pv_smem = ((size_t)TV_HD * TV_PSTRIDE + (size_t)mt_n * 16 * TV_PSTRIDE) * 2;
+    static bool attr_done = false;
+    if (!attr_done) {
+        Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_pv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        attr_done = true;
+    }
+    const size_t kv_layer = (size_t)D.kv_heads * in->max_ctx * TV_HD;
+    const size_t state_layer = (size_t)D.dn_v_heads * TV_DN * TV_DN;
+    const size_t nstate_layer = (size_t)in->max_nodes * state_layer, nconv_layer = (size_t)in->max_nodes * conv_ch;
+    if (in->max_nodes < n) { set_error("tree_verify: max_nodes %d < n_nodes %d", in->max_nodes, n); return QWEN35_ERR_BAD_ARG; }
+
+    tv_tree_prep_kernel<<<1, 32, 0, stream>>>(in->parents, n, s.depth, s.anc);
+    tv_embed_q4k_kernel<<<dim3(n, D.hidden / 256), 32, 0, stream>>>((const uint8_t*)in->token_embd, in->node_tokens, D.hidden, s.hidden);
+    g_launches.fetch_add(2);
+    const int n_layers = in->dbg_num_layers > 0 && in->dbg_num_layers < D.n_layers ? in->dbg_num_layers : D.n_layers;
+    int i_fa = 0, i_dn = 0;
+    for (int il = 0; il < n_layers; ++il) {
+        const Qwen35TreeLayer& W = in->layers[il];
+        const bool is_fa = (il % D.fa_period) == D.fa_period - 1;
+        if (il > 0 && in->dbg_teacher)
+            Q35_CUDA_OK(cudaMemcpyAsync(s.hidden, (const bf16*)in->dbg_teacher + (size_t)il * n * D.hidden, (size_t)n * D.hidden * 2, cudaMemcpyDeviceToDevice, stream));
+        tv_rmsnorm_kernel<<<n, 256, 0, stream>>>(s.hidden, (const float*)W.attn_norm, s.normed, D.hidden, D.eps);
+        g_launches.fetch_add(1);
+        int att_w;
+        if (is_fa) {
+            Q35_TRYT(q4k_linear(s.normed, D.hidden, (const uint8_t*)W.w_in, fa_in, D.hidden, s.proj, fa_in, nullptr, 0, n, 0, s.panel, stream));
+            bf16* kc = (bf16*)in->k_cache + (size_t)i_fa * kv_layer;
+            bf16* vc = (bf16*)in->v_cache + (size_t)i_fa * kv_layer;
+            tv_fa_prep_kernel<<<dim3(n, D.q_heads + 2 * D.kv_heads), 128, 0, stream>>>(s.proj, fa_in, (const float*)W.q_norm, (const float*)W.k_norm, s.depth, D,
+                                                                                       in->past, in->max_ctx, s.qbuf, kc, vc);
+            tv_att_scores_kernel<<<dim3(chunks, D.kv_heads), 256, sc_smem, stream>>>(s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores);
+            tv_att_stats_kernel<<<(D.kv_heads * R + 7) / 8, 256, 0, stream>>>(s.scores, D.kv_heads * R, lpad, chunks * TV_CHUNK, s.stats);
+            tv_att_pv_kernel<<<dim3(chunks, D.kv_heads), 256, pv_smem, stream>>>(vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial);
+            tv_att_merge_kernel<<<dim3(n, D.q_heads), 128, 0, stream>>>(s.partial, s.proj, fa_in, D, n, chunks, s.attn);
+            g_launches.fetch_add(5);
+            att_w = D.q_heads * TV_HD;
+            ++i_fa;
+        } else {
+            Q35_TRYT(q4k_linear(s.normed, D.hidden, (const uint8_t*)W.w_in, dn_in, D.hidden, s.proj, dn_in, nullptr, 0, n, 0, s.panel, stream));
+            Q35_TRYT(gemm_bf16(s.normed, D.hidden, (const bf16*)W.w_ba, 2 * D.dn_v_heads, s.ba, 2 * D.dn_v_heads, nullptr, 0, n, 2 * D.dn_v_heads, D.hidden, 0, 0, stream));
+            float* cstate = (float*)in->conv_state + (size_t)i_dn * 3 * conv_ch;
+            float* nconv = (float*)in->node_conv + (size_t)i_dn * nconv_layer;
+            __half* nstates = (__half*)in->node_states + (size_t)i_dn * nstate_layer;
+            tv_dn_conv_kernel<<<dim3(n, (conv_ch + 255) / 256), 256, 0, stream>>>(s.proj, dn_in, in->parents, cstate, (const float*)W.conv_w, conv_ch, s.dn_qkv, nconv);
+            tv_dn_norm_kernel<<<dim3(n, D.dn_k_heads), 128, 0, stream>>>(s.dn_qkv, conv_ch, s.ba, 2 * D.dn_v_heads, (const float*)W.ssm_a, (const float*)W.dt_bias, D, s.dn_gate);
+            tv_dn_tree_kernel<<<dim3(D.dn_v_heads, TV_DN / 16), 128, 0, stream>>>(s.dn_qkv, conv_ch, s.dn_gate, in->parents, n, D,
+                                                                                 (const float*)in->ssm_state + (size_t)i_dn * state_layer, nstates, s.core);
+            tv_dn_gated_norm_kernel<<<dim3(n, D.dn_v_heads), 128, 0, stream>>>(s.core, s.proj, dn_in, z_off, (const float*)W.ssm_norm, D, s.attn);
+            g_launches.fetch_add(4);
+            att_w = D.dn_v_heads * TV_DN;
+            ++i_dn;
+        }
+        Q35_TRYT(q4k_linear(s.attn, att_w, (const uint8_t*)W.w_out, D.hidden, att_w, s.resid, D.hidden, s.hidden, D.hidden, n, 1, s.panel, stream));
+        tv_rmsnorm_kernel<<<n, 256, 0, stream>>>(s.resid, (const float*)W.post_norm, s.normed, D.hidden, D.eps);
+        g_launches.fetch_add(1);
+        Q35_TRYT(q4k_linear(s.normed, D.hidden, (const uint8_t*)W.w_gate_up, D.ffn, D.hidden, s.mlp, D.ffn, nullptr, 0, n, 2, s.panel, stream));
+        Q35_TRYT(q4k_linear(s.mlp, D.ffn, (const uint8_t*)W.w_down, D.hidden, D.ffn, s.hidden, D.hidden, s.resid, D.hidden, n, 1, s.panel, stream));
+        if (in->dbg_hidden)
+            Q35_CUDA_OK(cudaMemcpyAsync((bf16*)in->dbg_hidden + (size_t)il * n * D.hidden, s.hidden, (size_t)n * D.hidden * 2, cudaMemcpyDeviceToDevice, stream));
+    }
+    tv_rmsnorm_kernel<<<n, 256, 0, stream>>>(s.hidden, (const float*)in->output_norm, s.normed, D.hidden, D.eps);
+    Q35_TRYT(q4k_linear(s.normed, D.hidden, (const uint8_t*)in->output_w, D.vocab, D.hidden, s.logits, D.vocab, nullptr, 0, n, 0, s.panel, stream));
+    tv_argmax_kernel<<<n, 1024, 0, stream>>>(s.logits, D.vocab, in->node_argmax);
+    g_launches.fetch_add(2);
+    if (in->logits_out) Q35_CUDA_OK(cudaMemcpyAsync(in->logits_out, s.logits, (size_t)n * D.vocab * 2, cudaMemcpyDeviceToDevice, stream));
+    Q35_CUDA_OK(cudaGetLastError());
+    return QWEN35_OK;
+}
+
+extern "C" int qwen35_b200_tree_accept(const int* node_tokens, const int* parents, const int* node_argmax, int n_nodes, int* path, int* result,
+                                       qwen35_stream_t stream) {
+    using namespace q35;
+    if (!node_tokens || !parents || !node_argmax || !path || !result || n_nodes <= 0 || n_nodes > 64) { set_error("tree_accept: bad arguments"); return QWEN35_ERR_BAD_ARG; }
+    tv_accept_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(node_tokens, parents, node_argmax, n_nodes, path, result);
+    Q35_CUDA_OK(cudaGetLastError());
+    g_launches.fetch_add(1);
+    return QWEN35_OK;
+}
+
+extern "C" int qwen35_b200_tree_commit(const Qwen35TreeVerifyArgs* in, const int* path, const int* result, qwen35_stream_t stream_) {
+    using namespace q35;
+    cudaStream_t stream = (cudaStream_t)stream_;
+    if (!in || !path || !result) { set_error("tree_commit: null args"); return QWEN35_ERR_BAD_ARG; }
+    const TvDims D = to_dims(&in->dims);
+    if (!tv_dims_ok(D)) { set_error("tree_commit: unsupported dimensions"); return QWEN35_ERR_BAD_ARG; }
+    int n_fa = 0;
+    for (int il = 0; il < D.n_layers; ++il) n_fa += (il % D.fa_period) == D.fa_period - 1;
+    const int n_dn = D.n_layers - n_fa;
+    const int conv_ch = (2 * D.dn_k_heads + D.dn_v_heads) * TV_DN;
+    const size_t state_layer = (size_t)D.dn_v_heads * TV_DN * TV_DN;
+    if (n_dn > 0) {
+        tv_commit_state_kernel<<<148 * 4, 256, 0, stream>>>((const __half*)in->node_states, (size_t)in->max_nodes * state_layer, state_layer, n_dn, path, result, (float*)in->ssm_state);
+        tv_commit_conv_kernel<<<148, 256, 0, stream>>>((const float*)in->node_conv, (size_t)in->max_nodes * conv_ch, conv_ch, n_dn, path, result, (float*)in->conv_state);
+    }
+    if (n_fa > 0)
+        tv_commit_kv_kernel<<<(n_fa * D.kv_heads * (TV_HD / 8) * 2 + 255) / 256, 256, 0, stream>>>((bf16*)in->k_cache, (bf16*)in->v_cache, (size_t)D.kv_heads * in->max_ctx * TV_HD,
+                                                                                                 n_fa, D.kv_heads, in->max_ctx, in->past, path, result);
+    Q35_CUDA_OK(cudaGetLastError());
+    g_launches.fetch_add(3);
+    return QWEN35_OK;
+}

@@ -59,6 +59,26 @@ class BatchedArgs(C.Structure):
     ]
 
 
+class TreeDimsC(C.Structure):
+    _fields_ = [(k, C.c_int) for k in ("n_layers", "hidden", "ffn", "vocab", "q_heads", "kv_heads", "head_dim", "dn_k_heads", "dn_v_heads",
+                                        "dn_dim", "rot_dim", "fa_period")] + [("rope_theta", C.c_float), ("rms_eps", C.c_float)]
+
+
+class TreeLayerC(C.Structure):
+    _fields_ = [(k, C.c_void_p) for k in ("attn_norm", "post_norm", "w_in", "w_ba", "w_out", "w_gate_up", "w_down", "q_norm", "k_norm", "conv_w",
+                                           "ssm_a", "dt_bias", "ssm_norm", "r0", "r1", "r2")]
+
+
+class TreeVerifyArgs(C.Structure):
+    _fields_ = [
+        ("dims", TreeDimsC), ("layers", C.POINTER(TreeLayerC)), ("token_embd", C.c_void_p), ("output_norm", C.c_void_p), ("output_w", C.c_void_p),
+        ("n_nodes", C.c_int), ("max_nodes", C.c_int), ("node_tokens", C.c_void_p), ("parents", C.c_void_p), ("past", C.c_int), ("max_ctx", C.c_int),
+        ("k_cache", C.c_void_p), ("v_cache", C.c_void_p), ("ssm_state", C.c_void_p), ("conv_state", C.c_void_p), ("node_states", C.c_void_p),
+        ("node_conv", C.c_void_p), ("node_argmax", C.c_void_p), ("logits_out", C.c_void_p), ("dbg_hidden", C.c_void_p), ("dbg_num_layers", C.c_int),
+        ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t), ("dbg_teacher", C.c_void_p),
+    ]
+
+
 _lib = None
 
 # name -> (restype, argtypes); every symbol include/qwen35_b200.h declares
@@ -77,6 +97,11 @@ SIGNATURES = {
     "launch_quantize_nvfp4_lm_out": (_i, [_vp, _i, _i, _vp, _vp, _vp]),
     "qwen35_b200_decode_batched": (_i, [C.POINTER(BatchedArgs), _vp]),
     "qwen35_b200_forget_tables": (None, []),
+    "qwen35_b200_tree_scratch_bytes": (C.c_size_t, [C.POINTER(TreeDimsC), _i, _i]),
+    "qwen35_b200_tree_verify": (_i, [C.POINTER(TreeVerifyArgs), _vp]),
+    "qwen35_b200_tree_accept": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp]),
+    "qwen35_b200_tree_commit": (_i, [C.POINTER(TreeVerifyArgs), _vp, _vp, _vp]),
+    "qwen35_b200_dequant_q4k": (_i, [_vp, C.c_size_t, _vp, _vp, _vp]),
     "qwen35_b200_gemm_bf16": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "qwen35_b200_status": (_i, [_vp]),
     "qwen35_b200_clear_status": (_i, [_vp]),

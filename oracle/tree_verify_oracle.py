@@ -1,0 +1,211 @@
+"""TEST INFRASTRUCTURE ONLY: CPU oracle of the tree-verify pass (imported by tests/, __graft_entry__.smoke() and the
+cpu_baseline leg of bench.py, never by the product).
+
+Parity status: **parity unpinned** for the forward arithmetic.  The reference builds this pass from ggml operators of
+a llama.cpp fork (submodule `deps/llama.cpp`, https://github.com/Luce-Org/llama.cpp.git branch luce-dflash, no commit
+recorded, directory empty in the reference checkout), and its own tests store no expected values for it
+(models/qwen35_27b/test/smoke_target_forward.cpp:7-8).  What IS pinned: the Q4_K unpacking, against gguf-py 0.19.0
+`gguf.quants.dequantize` (tests/test_q4k_oracle.py).  The rest restates the graph semantics of
+models/qwen35_27b/src/qwen35_target_graph.cpp:281-804 and the tree semantics of models/qwen35_27b/test/test_dflash.cpp
+:396-442, 1355-1521 as "a node's result is the sequential model run on its root-to-node token path", written
+path-recursively (no mask, no DFS tricks) so it checks the mask / parent-chain logic of the product independently.
+
+Rounding points (shared with the product by definition, since nothing upstream pins them): activations between
+operators are bf16; a Q4_K linear uses bf16(dequantised weight) with f32 accumulation and returns bf16; norms, RoPE,
+softmax, conv, the delta rule and its state are f32; attention probabilities are rounded to bf16 before P.V; a node's
+DeltaNet post-state is kept as f16 and a node that is not its parent's first child (DFS index parent+1) starts from
+that f16 copy (qwen35_target_graph.cpp:540-583: the kernel reloads state at DFS branch transitions)."""
+import numpy as np
+import torch
+
+
+def q4k_dequant(blocks: np.ndarray) -> np.ndarray:
+    """[n, 144] uint8 -> [n, 256] f32: y = (d*sc)*q - (dmin*m), sub-block j of 32 weights uses scale/min j; the low
+    nibbles of bytes 32g..32g+31 are weights 64g..64g+31, the high nibbles weights 64g+32..64g+63."""
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1, 144)
+    n = blocks.shape[0]
+    d = blocks[:, 0:2].copy().view(np.float16).astype(np.float32).reshape(n)
+    dmin = blocks[:, 2:4].copy().view(np.float16).astype(np.float32).reshape(n)
+    s = blocks[:, 4:16].astype(np.int32)
+    sc = np.zeros((n, 8), np.int32); mn = np.zeros((n, 8), np.int32)
+    for j in range(8):
+        if j < 4:
+            sc[:, j] = s[:, j] & 63; mn[:, j] = s[:, j + 4] & 63
+        else:
+            sc[:, j] = (s[:, j + 4] & 0xF) | ((s[:, j - 4] >> 6) << 4)
+            mn[:, j] = (s[:, j + 4] >> 4) | ((s[:, j] >> 6) << 4)
+    qs = blocks[:, 16:144]
+    out = np.zeros((n, 256), np.float32)
+    for g in range(4):
+        q = qs[:, 32 * g:32 * g + 32]
+        for half, vals in ((0, q & 0xF), (1, q >> 4)):
+            j = 2 * g + half
+            dj = (d * sc[:, j].astype(np.float32)).astype(np.float32)[:, None]
+            mj = (dmin * mn[:, j].astype(np.float32)).astype(np.float32)[:, None]
+            out[:, 64 * g + 32 * half:64 * g + 32 * half + 32] = (dj * vals.astype(np.float32)).astype(np.float32) - mj
+    return out
+
+
+def rb(x: torch.Tensor) -> torch.Tensor:
+    return x.bfloat16().float()
+
+
+class TreeOracle:
+    def __init__(self, dims, weights, max_ctx):
+        """weights: the dict of qwen35_b200.tree_verify.make_random_tree_weights on the CPU."""
+        self.D, self.max_ctx = dims, max_ctx
+        D = dims
+
+        def mat(blocks):
+            r, nb, _ = blocks.shape
+            return rb(torch.from_numpy(q4k_dequant(blocks.numpy().reshape(-1, 144))).reshape(r, nb * 256))
+
+        self.layers = []
+        for L in weights["layers"]:
+            M = {k: (mat(v) if v.dtype == torch.uint8 else v.float()) for k, v in L.items()}
+            self.layers.append(M)
+        self.embd_blocks = weights["token_embd"]
+        self.output_norm = weights["output_norm"].float()
+        self.output_w = mat(weights["output_w"])
+        # committed context
+        self.k = [torch.zeros(D.kv_heads, 0, D.head_dim) for _ in range(D.n_fa)]
+        self.v = [torch.zeros(D.kv_heads, 0, D.head_dim) for _ in range(D.n_fa)]
+        self.ssm = [torch.zeros(D.dn_v_heads, D.dn_dim, D.dn_dim) for _ in range(D.n_dn)]       # [head][value][key]
+        self.conv = [torch.zeros(3, D.conv_ch) for _ in range(D.n_dn)]                           # row 2 newest
+        self.past = 0
+
+    # ---- one token through the model, from an explicit context; returns logits and the new context ----
+    def _norm(self, x, w):
+        return rb(x * torch.rsqrt((x * x).mean() + self.D.rms_eps) * w)
+
+    def _rope(self, x, pos):
+        D = self.D
+        half = D.rot_dim // 2
+        i = torch.arange(half, dtype=torch.float32)
+        inv = torch.pow(torch.tensor(D.rope_theta, dtype=torch.float32), -(2 * i) / D.rot_dim)
+        ang = (torch.tensor(float(pos), dtype=torch.float32) * inv)
+        c, s = torch.cos(ang), torch.sin(ang)
+        y = x.clone()
+        y[..., :half] = x[..., :half] * c - x[..., half:D.rot_dim] * s
+        y[..., half:D.rot_dim] = x[..., half:D.rot_dim] * c + x[..., :half] * s
+        return y
+
+    def step(self, token, ctx, pos):
+        """ctx = dict(k, v: lists [kv, len, 256] bf16-valued f32; ssm: list f32; conv: list [3, ch]).  Returns
+        (logits bf16-valued f32 [vocab], new ctx, per-layer hidden list)."""
+        D = self.D
+        nb = D.hidden // 256
+        x = rb(torch.from_numpy(q4k_dequant(self.embd_blocks[token].numpy().reshape(nb, 144))).reshape(D.hidden))
+        new = {"k": [], "v": [], "ssm": [], "conv": []}
+        hid = []
+        i_fa = i_dn = 0
+        for il, W in enumerate(self.layers):
+            n = self._norm(x, W["attn_norm"])
+            proj = rb(W["w_in"] @ n)
+            if D.is_fa(il):
+                qg = proj[:2 * D.q_heads * 256].reshape(D.q_heads, 2, 256)
+                q, gate = qg[:, 0], qg[:, 1]
+                kk = proj[2 * D.q_heads * 256:2 * D.q_heads * 256 + D.kv_heads * 256].reshape(D.kv_heads, 256)
+                vv = proj[2 * D.q_heads * 256 + D.kv_heads * 256:].reshape(D.kv_heads, 256)
+                hn = lambda t, w: t * torch.rsqrt((t * t).mean(-1, keepdim=True) + D.rms_eps) * w      # noqa: E731
+                q = rb(self._rope(hn(q, W["q_norm"]), pos))
+                kk = rb(self._rope(hn(kk, W["k_norm"]), pos))
+                K = torch.cat([ctx["k"][i_fa], kk[:, None]], 1); V = torch.cat([ctx["v"][i_fa], vv[:, None]], 1)
+                new["k"].append(K); new["v"].append(V)
+                gqa = D.q_heads // D.kv_heads
+                out = torch.zeros(D.q_heads, 256)
+                for h in range(D.q_heads):
+                    s = (K[h // gqa] @ q[h]) * 0.0625
+                    p = torch.exp(s - s.max()); p = rb(p / p.sum())
+                    out[h] = p @ V[h // gqa]
+                att = rb(out * torch.sigmoid(gate)).reshape(-1)
+                i_fa += 1
+            else:
+                xin = proj[:D.conv_ch]; z = proj[D.conv_ch:].reshape(D.dn_v_heads, D.dn_dim)
+                ba = rb(W["w_ba"] @ n)
+                win = torch.cat([ctx["conv"][i_dn], xin[None]], 0)                                    # [4, ch]
+                cw = W["conv_w"]
+                s = cw[:, 0] * win[0]
+                for t in (1, 2, 3):
+                    s = torch.addcmul(s, cw[:, t], win[t])
+                c = s * torch.sigmoid(s)
+                new["conv"].append(win[1:].clone())
+                nk = D.dn_k_heads * D.dn_dim
+                q = c[:nk].reshape(D.dn_k_heads, D.dn_dim); k = c[nk:2 * nk].reshape(D.dn_k_heads, D.dn_dim)
+                v = c[2 * nk:].reshape(D.dn_v_heads, D.dn_dim)
+                q = q * torch.rsqrt((q * q).sum(-1, keepdim=True) + D.rms_eps) * 0.08838834764831845
+                k = k * torch.rsqrt((k * k).sum(-1, keepdim=True) + D.rms_eps)
+                beta = torch.sigmoid(ba[:D.dn_v_heads])
+                a = ba[D.dn_v_heads:] + W["dt_bias"]
+                sp = torch.where(a > 20, a, torch.log1p(torch.exp(a)))
+                decay = torch.exp(sp * W["ssm_a"])
+                S = ctx["ssm"][i_dn].clone()
+                o = torch.zeros(D.dn_v_heads, D.dn_dim)
+                for h in range(D.dn_v_heads):
+                    kh = h % D.dn_k_heads
+                    Sh = S[h] * decay[h]
+                    kv = Sh @ k[kh]
+                    delta = (v[h] - kv) * beta[h]
+                    Sh = Sh + delta[:, None] * k[kh][None, :]
+                    o[h] = Sh @ q[kh]
+                    S[h] = Sh
+                new["ssm"].append(S)
+                inv = torch.rsqrt((o * o).mean(-1, keepdim=True) + D.rms_eps)
+                att = rb(o * inv * W["ssm_norm"] * (z * torch.sigmoid(z))).reshape(-1)
+                i_dn += 1
+            r = rb(rb(W["w_out"] @ att) + x)
+            n2 = self._norm(r, W["post_norm"])
+            g = rb(W["w_gate_up"][:D.ffn] @ n2); u = rb(W["w_gate_up"][D.ffn:] @ n2)
+            m = rb(rb(g * torch.sigmoid(g)) * u)
+            x = rb(rb(W["w_down"] @ m) + r)
+            hid.append(x.clone())
+        logits = rb(self.output_w @ self._norm(x, self.output_norm))
+        return logits, new, hid
+
+    def context(self):
+        return {"k": self.k, "v": self.v, "ssm": self.ssm, "conv": self.conv}
+
+    def feed(self, tokens):
+        """Sequentially extend the committed context (f32 state, no f16 rounding)."""
+        for t in tokens:
+            _, ctx, _ = self.step(int(t), self.context(), self.past)
+            self.k, self.v, self.ssm, self.conv = ctx["k"], ctx["v"], ctx["ssm"], ctx["conv"]
+            self.past += 1
+
+    def verify(self, tokens, parents):
+        """Per-node logits, per-node contexts (post-state as the product persists it) and hidden traces."""
+        n = len(tokens)
+        children = [[] for _ in range(n)]
+        for t in range(1, n):
+            children[parents[t]].append(t)
+        logits, ctxs, hids, depth = [None] * n, [None] * n, [None] * n, [0] * n
+
+        def run(t, ctx_in):
+            logits[t], c, hids[t] = self.step(int(tokens[t]), ctx_in, self.past + depth[t])
+            ctxs[t] = c
+            for ch in children[t]:
+                depth[ch] = depth[t] + 1
+                if ch == t + 1:
+                    cin = c
+                else:                      # DFS branch transition: the child starts from the persisted f16 state
+                    cin = dict(c); cin["ssm"] = [s.half().float() for s in c["ssm"]]
+                run(ch, cin)
+
+        run(0, self.context())
+        return logits, ctxs, hids
+
+    @staticmethod
+    def accept(tokens, parents, argmax):
+        path, cur = [0], 0
+        while True:
+            nxt = [c for c in range(cur + 1, len(tokens)) if parents[c] == cur and int(tokens[c]) == int(argmax[cur])]
+            if not nxt:
+                break
+            cur = nxt[0]; path.append(cur)
+        return path, int(argmax[cur])
+
+    def commit(self, ctxs, path):
+        leaf = ctxs[path[-1]]
+        self.k, self.v, self.conv = leaf["k"], leaf["v"], leaf["conv"]
+        self.ssm = [s.half().float() for s in leaf["ssm"]]
+        self.past += len(path)

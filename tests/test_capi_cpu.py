@@ -18,7 +18,7 @@ from qwen35_b200.weights import make_random_weights, make_token_ids
 def _declared_functions():
     text = open(os.path.join(ROOT, "include", "qwen35_b200.h")).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    names = re.findall(r"^\s*(?:const\s+)?(?:int|long long|char\s*\*|void)\s*\*?\s*(\w+)\s*\(", text, flags=re.M)
+    names = re.findall(r"^\s*(?:const\s+)?(?:int|long long|size_t|char\s*\*|void)\s*\*?\s*(\w+)\s*\(", text, flags=re.M)
     return sorted(set(names))
 
 

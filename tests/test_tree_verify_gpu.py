@@ -1,0 +1,141 @@
+"""GPU parity of the tree-verify pass (qwen35_b200_tree_verify / _accept / _commit / _dequant_q4k, through the C ABI)
+against the path-sequential CPU oracle, at reduced widths so the oracle finishes in seconds."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 3e-2          # bf16 logits of magnitude ~1: a few last-place flips through 4 layers
+# States and per-layer outputs are compared TEACHER FORCED (every layer reads the oracle's input for that layer), as in
+# the other parity tests: free running, a last-place bf16 flip in one layer's output perturbs every later layer's
+# q/k/v and the state error grows layer by layer (measured 2e-4, 2e-3, 5e-3 over three DeltaNet layers).  Teacher
+# forced the state carries only f16 storage (2^-11) and the flips of its own projection.
+STATE_REL_TOL = 1e-3
+LAYER_ABS_TOL = 2.0 ** -5
+
+
+def small_dims():
+    from qwen35_b200.tree_verify import TreeDims
+    return TreeDims(n_layers=4, hidden=512, ffn=1024, vocab=2048, q_heads=4, kv_heads=2, dn_k_heads=2, dn_v_heads=4)
+
+
+def test_q4k_dequant_gpu_bit_exact():
+    from oracle.tree_verify_oracle import q4k_dequant
+    from qwen35_b200.tree_verify import dequant_q4k, random_q4k
+    b = random_q4k(37, 512, 5).reshape(-1, 144).clone()
+    b[0, 4:16] = 0xFF; b[1, 4:16] = 0; b[2, 16:] = 0xFF; b[3, 16:] = 0; b[6, 0:4] = 0
+    b[4, 0:2] = torch.from_numpy(np.array([-0.5], np.float16).view(np.uint8))
+    ref = torch.from_numpy(q4k_dequant(b.numpy()))
+    got = dequant_q4k(b.cuda(), "f32").cpu()
+    assert torch.equal(got.view(torch.int32), ref.view(torch.int32))
+    got16 = dequant_q4k(b.cuda(), "bf16").cpu()
+    assert torch.equal(got16.view(torch.int16), ref.bfloat16().view(torch.int16))
+
+
+def _setup(n_ctx, seed):
+    from oracle.tree_verify_oracle import TreeOracle
+    from qwen35_b200.tree_verify import TreeTarget, make_random_tree_weights
+    D = small_dims()
+    w = make_random_tree_weights(D, seed)
+    orc = TreeOracle(D, w, 256)
+    rng = np.random.default_rng(seed)
+    orc.feed(rng.integers(0, D.vocab, n_ctx))
+    wg = {"layers": [{k: v.cuda() for k, v in L.items()} for L in w["layers"]],
+          "token_embd": w["token_embd"].cuda(), "output_norm": w["output_norm"].cuda(), "output_w": w["output_w"].cuda()}
+    tt = TreeTarget(D, wg, max_ctx=256)
+    for i in range(D.n_fa):
+        tt.k_cache[i, :, :n_ctx] = orc.k[i].bfloat16().cuda(); tt.v_cache[i, :, :n_ctx] = orc.v[i].bfloat16().cuda()
+    for i in range(D.n_dn):
+        tt.ssm_state[i] = orc.ssm[i].cuda(); tt.conv_state[i] = orc.conv[i].cuda()
+    tt.past = n_ctx
+    return D, orc, tt, rng
+
+
+@pytest.mark.parametrize("n_ctx,n_nodes,max_depth,seed", [(70, 14, 5, 1), (3, 1, 1, 2), (130, 33, 8, 3), (0, 6, 6, 4)])
+def test_tree_verify_matches_path_sequential_oracle(n_ctx, n_nodes, max_depth, seed):
+    from qwen35_b200.tree_verify import random_tree
+    D, orc, tt, rng = _setup(n_ctx, seed)
+    parents = random_tree(n_nodes, max_depth, seed) if n_nodes > 1 else [-1]
+    if seed == 4:
+        parents = [-1] + list(range(n_nodes - 1))          # a pure chain: the tree pass equals sequential decoding
+    tokens = rng.integers(0, D.vocab, n_nodes)
+    ref_logits, ctxs, hids = orc.verify(tokens, parents)
+    teacher = torch.zeros(D.n_layers, n_nodes, D.hidden, dtype=torch.bfloat16)
+    for t in range(n_nodes):
+        for il in range(1, D.n_layers):
+            teacher[il, t] = hids[t][il - 1].bfloat16()
+    dbg = torch.zeros(D.n_layers, n_nodes, D.hidden, dtype=torch.bfloat16, device="cuda")
+    tk, pr = torch.tensor(tokens, dtype=torch.int32), torch.tensor(parents, dtype=torch.int32)
+    tt.verify(tk, pr, dbg_hidden=dbg, dbg_teacher=teacher.cuda())
+    tt.check_status()
+    got_h = dbg.float().cpu()
+    i_dn = [il for il in range(D.n_layers) if not D.is_fa(il)]
+    worst_state = 0.0
+    for t in range(n_nodes):
+        for il in range(D.n_layers):
+            assert float((got_h[il, t] - hids[t][il]).abs().max()) <= LAYER_ABS_TOL, (t, il)
+        for j, il in enumerate(i_dn):
+            ref_s = ctxs[t]["ssm"][j]
+            got_s = tt.node_states[j, t].float().cpu()
+            worst_state = max(worst_state, float((got_s - ref_s).norm() / ref_s.norm().clamp_min(1e-6)))
+    exact = float((got_h == torch.stack([torch.stack(h) for h in hids]).transpose(0, 1)).float().mean())
+    print(f"teacher forced: {exact:.4%} of layer outputs bit-identical, worst node-state rel error {worst_state:.2e}")
+    assert worst_state <= STATE_REL_TOL
+    # free running: logits and arg-max
+    logits = torch.zeros(n_nodes, D.vocab, dtype=torch.bfloat16, device="cuda")
+    am = tt.verify(tk, pr, logits_out=logits).cpu().clone()
+    tt.check_status()
+    got_l = logits.float().cpu()
+    for t in range(n_nodes):
+        dl = (got_l[t] - ref_logits[t]).abs()
+        assert float(dl.max()) <= LOGIT_TOL, (t, float(dl.max()))
+        top = torch.topk(ref_logits[t], 2).values
+        if float(top[0] - top[1]) > 2 * LOGIT_TOL:
+            assert int(am[t]) == int(ref_logits[t].argmax())
+    # accepted path: force arg-max values so that a known root-to-node chain is taken, then commit and compare
+    children = {t: [c for c in range(n_nodes) if parents[c] == t] for t in range(n_nodes)}
+    want, cur = [0], 0
+    forced = am.clone()
+    while children[cur] and len(want) < 4:
+        nxt = children[cur][-1]                                   # the LAST child: exercises the DFS branch reload
+        forced[cur] = int(tokens[nxt])
+        # an earlier sibling with the same token would win the walk; make sure none has it
+        if any(int(tokens[c]) == int(tokens[nxt]) for c in children[cur][:-1]):
+            break
+        cur = nxt; want.append(cur)
+    if children[cur]:
+        forced[cur] = (max(int(tokens[c]) for c in children[cur]) + 1) % D.vocab if all((max(int(tokens[c]) for c in children[cur]) + 1) % D.vocab != int(tokens[c]) for c in children[cur]) else forced[cur]
+    tt.node_argmax[:n_nodes] = forced.cuda()
+    path, result = tt.accept()
+    from oracle.tree_verify_oracle import TreeOracle
+    ref_path, ref_next = TreeOracle.accept(tokens, parents, forced.tolist())
+    res = result.cpu().tolist()
+    assert res[0] == len(ref_path) and path[:res[0]].cpu().tolist() == ref_path and res[1] == ref_next
+    n_acc = tt.commit()
+    orc.commit(ctxs, ref_path)
+    assert n_acc == len(ref_path) and tt.past == orc.past
+    for i in range(D.n_fa):
+        assert float((tt.k_cache[i, :, :tt.past].float().cpu() - orc.k[i]).abs().max()) <= 2.0 ** -5
+        assert float((tt.v_cache[i, :, :tt.past].float().cpu() - orc.v[i]).abs().max()) <= 2.0 ** -5
+    for j in range(D.n_dn):      # free running here: see the note at STATE_REL_TOL
+        assert float((tt.ssm_state[j].cpu() - orc.ssm[j]).norm() / orc.ssm[j].norm().clamp_min(1e-6)) <= 1e-2
+        assert float((tt.conv_state[j].cpu() - orc.conv[j]).abs().max()) <= 2.0 ** -6
+    # a second tree on top of the committed state keeps working (state hand-over through the commit)
+    tokens2 = rng.integers(0, D.vocab, 3)
+    ref2, _, _ = orc.verify(tokens2, [-1, 0, 0])
+    l2 = torch.zeros(3, D.vocab, dtype=torch.bfloat16, device="cuda")
+    tt.verify(torch.tensor(tokens2, dtype=torch.int32), torch.tensor([-1, 0, 0], dtype=torch.int32), logits_out=l2)
+    tt.check_status()
+    for t in range(3):
+        assert float((l2[t].float().cpu() - ref2[t]).abs().max()) <= 2 * LOGIT_TOL
+
+
+def test_tree_verify_argument_checks():
+    from qwen35_b200._capi import Qwen35Error
+    D, orc, tt, rng = _setup(2, 9)
+    with pytest.raises(Qwen35Error):          # more nodes than the library's limit
+        tt.verify(torch.zeros(41, dtype=torch.int32), torch.full((41,), -1, dtype=torch.int32))
+    tt.past = 250
+    with pytest.raises(Qwen35Error):          # past + nodes beyond the cache
+        tt.verify(torch.zeros(10, dtype=torch.int32), torch.tensor([-1] + list(range(9)), dtype=torch.int32))
