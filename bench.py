@@ -149,6 +149,47 @@ def prefill_sweep(weights_gpu, dev, lengths):
     return out
 
 
+def tree_verify_bench(dev, n_nodes=33, ctx=4096, iters=5):
+    """27B-class dims, Q4_K weights generated directly as random super-blocks (dequantised
+    sigma ~0.02), a 4096-token context of random cache contents, one 33-node tree (seeded random parents, depth <= 8):
+    milliseconds per verify + accept walk + commit, timed with CUDA events."""
+    from qwen35_b200.tree_verify import QWEN35_27B as T, TreeTarget, make_random_tree_weights, random_tree
+    w = make_random_tree_weights(T, 11, device=dev)
+    tt = TreeTarget(T, w, max_ctx=ctx + 128, device=dev)
+    g = torch.Generator(device=dev).manual_seed(11)
+    tt.k_cache.copy_(torch.randn(tt.k_cache.shape, device=dev, generator=g).bfloat16())
+    tt.v_cache.copy_(torch.randn(tt.v_cache.shape, device=dev, generator=g).bfloat16())
+    tt.ssm_state.copy_(0.01 * torch.randn(tt.ssm_state.shape, device=dev, generator=g))
+    tt.conv_state.copy_(0.1 * torch.randn(tt.conv_state.shape, device=dev, generator=g))
+    parents = torch.tensor(random_tree(n_nodes, 8, 11), dtype=torch.int32, device=dev)
+    tokens = torch.randint(0, T.vocab, (n_nodes,), dtype=torch.int32, device=dev, generator=g)
+    times, acc = [], 0
+    lib = tt._lib
+    l0 = lib.qwen35_b200_launch_count()
+    for i in range(3 + iters):
+        tt.past = ctx
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        tt.verify(tokens, parents)
+        tt.accept()
+        acc = tt.commit()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        if i >= 3:
+            times.append(e0.elapsed_time(e1))
+    tt.check_status()
+    launches = (lib.qwen35_b200_launch_count() - l0) // (3 + iters)
+    ms = min(times)
+    w_bytes = (24_352_522_240 + 1_271_398_400) * 0.5625
+    kv_bytes = T.n_fa * T.kv_heads * (ctx + n_nodes) * T.head_dim * 2 * 2
+    st_bytes = T.n_dn * n_nodes * T.dn_v_heads * T.dn_dim * T.dn_dim * 2
+    alg = w_bytes + kv_bytes + st_bytes
+    flops = 2 * (24_352_522_240 + 1_271_398_400) * n_nodes
+    return {"workload": "BASELINE configs[4]: 27B-class dims (64 layers, hidden 5120), Q4_K weights, %d-token context, %d-node tree" % (ctx, n_nodes),
+            "ms_per_verify_commit": ms, "accepted": acc, "launches_per_pass": int(launches), "algorithmic_bytes": alg, "hbm_gbs": alg / (ms * 1e-3) / 1e9,
+            "roofline_frac": alg / (ms * 1e-3) / 1e9 / measured_peak()[0], "tflops": flops / (ms * 1e-3) / 1e12}
+
+
 def batched_decode_bench(weights_gpu, dev, rank, n_seq, ctx, n_steps):
     """`n_seq` independent sequences per GPU, `ctx`-token contexts prefilled by the library's own
     prefill, `n_steps` greedy steps.  Returns (tok/s on this rank, ms per step, algorithmic bytes per step)."""
@@ -341,6 +382,9 @@ def run_ours(args):
     sweep = None
     if args.prefill_sweep and rank == 0:
         sweep = prefill_sweep(wg, dev, [int(x) for x in args.prefill_sweep.split(",")])
+    tree = None
+    if args.tree_verify and rank == 0:
+        tree = tree_verify_bench(dev)
     batched = None
     if args.batched > 0:
         b_tok_s, b_ms, b_bytes = batched_decode_bench(wg, dev, rank, args.batched, args.batched_ctx, GEN)
@@ -401,6 +445,8 @@ def run_ours(args):
             line["batched_decode"] = batched
         if sweep:
             line["prefill_sweep"] = sweep
+        if tree:
+            line["tree_verify"] = tree
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(w_cpu, ids_cpu, 16, use_hf=False)
         print(json.dumps(line))
@@ -417,6 +463,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batched", type=int, default=64, help="sequences per GPU for the batched-decode section (0 = skip)")
     ap.add_argument("--batched-ctx", type=int, default=2048)
+    ap.add_argument("--prefill-sweep", default="128,512,1024,4096", help="prompt lengths of the prefill sweep ('' = skip)")
+    ap.add_argument("--tree-verify", type=int, default=1, help="run the 27B-class tree-verify section (0 = skip)")
     ap.add_argument("--prompt", type=int, default=520, help="prompt tokens (smaller values are for profiler captures)")
     ap.add_argument("--gen", type=int, default=128, help="decode tokens per step")
     args = ap.parse_args()
