@@ -299,6 +299,12 @@ void qwen35_b200_forget_tables(void);
 int qwen35_b200_gemm_bf16(const void* A, int lda, const void* B, int b_rows, void* C, int ldc, const void* R, int ldr,
                           int M, int N, int K, int epilogue, int up_row_offset, qwen35_stream_t stream);
 
+/* The same contraction with Q4_K weights (W = super-blocks [w_rows][K/256][144]), dequantised inside the kernel
+ * (the role of ggml_mul_mat on a K-quant tensor, qwen35_target_graph.cpp:262-273, 295-404, 438-661).  M <= 128,
+ * K a multiple of 256; rows of W beyond w_rows read as zero. */
+int qwen35_b200_gemm_q4k(const void* A, int lda, const void* W, int w_rows, void* C, int ldc, const void* R, int ldr,
+                         int M, int N, int K, int epilogue, int up_row_offset, qwen35_stream_t stream);
+
 /* No counterpart in the reference.  qwen35_b200_decode_steps for callers that must not allocate: an
  * inference server that hands all device memory to its own pool at start-up (a later cudaMalloc inside a
  * library can then fail or fragment the pool), or a latency-critical loop in which the device-wide

@@ -17,6 +17,7 @@
 // applies the epilogue.  No partial sums go through global memory and no second kernel runs.
 // Every wait is bounded; a wait that runs out sets the status word and the CTA unwinds normally.
 #include <cuda.h>
+#include <cuda_fp16.h>
 
 #include "common.cuh"
 #include "runtime.h"
@@ -335,6 +336,261 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
     }
 }
 
+// ------------------------------------------------------------------------------------------------------------
+// Q4_K weights: C[M <= 128, N] = epi(A[M, K] . dequant(W[N, K])^T).  Same pipeline as the split-K kernel above, but
+// the weight operand never exists in global memory as bf16: eight dequantisation warps read the 4.5-bit super-blocks
+// and write bf16(value) straight into the 128-byte-swizzled shared-memory tile the MMA descriptor expects.
+// A 64-wide k-step of one weight row is exactly one 64-weight group of a Q4_K super-block (32 nibble bytes, two
+// 6-bit scale/min pairs), so one thread dequantises one tile row per k-step: 2 x 16-byte loads + the 16-byte header.
+//   warp 0      TMA producer of the activation tile        warp 1   MMA issue (waits for both operands of a stage)
+//   warps 2-5   dequantise even k-steps, then the epilogue  warps 6-9 dequantise odd k-steps
+// value = bf16((d*sc)*q - dmin*m) with separate f32 roundings, the published Q4_K dequantisation.
+constexpr int Q4K_THREADS = 320;
+constexpr int Q4K_STAGES = 3;
+constexpr uint32_t Q4K_SMEM = Q4K_STAGES * GEMM_STAGE_BYTES + 1024 + 256;
+
+__device__ __forceinline__ void q4k_scale_min_u32(uint32_t s0, uint32_t s1, uint32_t s2, int j, float& sc, float& mn) {
+    // s0, s1, s2 = scale bytes 0-3, 4-7, 8-11
+    const uint32_t bj = (j < 4) ? (s0 >> (8 * j)) & 0xFF : (s1 >> (8 * (j - 4))) & 0xFF;          // scales[j]
+    if (j < 4) {
+        const uint32_t bj4 = (s1 >> (8 * j)) & 0xFF;                                                // scales[j+4]
+        sc = (float)(bj & 63); mn = (float)(bj4 & 63);
+    } else {
+        const uint32_t bj4 = (s2 >> (8 * (j - 4))) & 0xFF;                                          // scales[j+4]
+        const uint32_t bjm = (s0 >> (8 * (j - 4))) & 0xFF;                                          // scales[j-4]
+        sc = (float)((bj4 & 0xF) | ((bjm >> 6) << 4)); mn = (float)((bj4 >> 4) | ((bj >> 6) << 4));
+    }
+}
+
+struct Q4kParams {
+    GemmParams g;
+    const uint8_t* W;       // super-blocks, row-major [rows][K/256][144]
+    int w_rows;             // rows that exist in W (rows beyond read as zero)
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(Q4K_THREADS, 2)
+gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const Q4kParams qp) {
+    const GemmParams& p = qp.g;
+    constexpr int STAGES = Q4K_STAGES;
+    extern __shared__ unsigned char g_smem_raw[];
+    const uint32_t raw = g_smem_u32(g_smem_raw);
+    const uint32_t tiles = (raw + 1023u) & ~1023u;
+    unsigned char* tiles_ptr = g_smem_raw + (tiles - raw);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(tiles_ptr + STAGES * GEMM_STAGE_BYTES);
+    const uint32_t fulla0 = g_smem_u32(bars), fullb0 = fulla0 + 8 * STAGES, empty0 = fullb0 + 8 * STAGES, tfull = empty0 + 8 * STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 1);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int BN_OUT = (EPI == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
+    const int n0 = blockIdx.x * BN_OUT;
+    const int nkb_all = p.K / GEMM_BK;
+    const int S = (int)gridDim.z, z = (int)blockIdx.z;
+    const int kb_begin = (int)(((long long)z * nkb_all) / S), kb_end = (int)(((long long)(z + 1) * nkb_all) / S);
+    const int nkb = kb_end - kb_begin;
+
+    if (threadIdx.x == 0) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+        *s_abort = 0;
+        for (int i = 0; i < STAGES; ++i) { g_mbar_init(fulla0 + 8 * i, 1); g_mbar_init(fullb0 + 8 * i, 4); g_mbar_init(empty0 + 8 * i, 1); }
+        g_mbar_init(tfull, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(g_smem_u32(tmem_slot)), "r"(128u) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int issued = 0;
+            for (int i = 0; i < nkb; ++i) {
+                const int st = i % STAGES;
+                if (!g_mbar_wait(empty0 + 8 * st, ((i / STAGES) & 1) ^ 1, p.err, s_abort)) break;
+                g_mbar_expect_tx(fulla0 + 8 * st, GEMM_BM * GEMM_BK * 2);
+                g_tma_load_2d(tiles + st * GEMM_STAGE_BYTES, &tmA, (kb_begin + i) * GEMM_BK, 0, fulla0 + 8 * st);
+                issued = i + 1;
+            }
+            if (*s_abort) {
+                for (int i = max(0, issued - STAGES); i < issued; ++i) {
+                    unsigned it = 0;
+                    while (!g_mbar_try_wait(fulla0 + 8 * (i % STAGES), (i / STAGES) & 1) && ++it < GEMM_SPIN_LIMIT) {}
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            for (int i = 0; i < nkb; ++i) {
+                const int st = i % STAGES;
+                if (!g_mbar_wait(fulla0 + 8 * st, (i / STAGES) & 1, p.err, s_abort)) break;
+                if (!g_mbar_wait(fullb0 + 8 * st, (i / STAGES) & 1, p.err, s_abort)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t a_addr = tiles + st * GEMM_STAGE_BYTES, b_addr = a_addr + GEMM_BM * GEMM_BK * 2;
+                const uint64_t adesc = make_smem_desc(a_addr), bdesc = make_smem_desc(b_addr);
+#pragma unroll
+                for (int k = 0; k < GEMM_BK / 16; ++k)
+                    umma_bf16(tmem_base, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), GEMM_IDESC, (i > 0 || k > 0) ? 1u : 0u);
+                umma_commit(empty0 + 8 * st);
+            }
+            umma_commit(tfull);
+        }
+    } else {
+        // ---- dequantisation: group 0 (warps 2-5) even k-steps, group 1 (warps 6-9) odd k-steps; thread = tile row ----
+        const int grp = (warp - 2) >> 2, r = ((warp - 2) & 3) * 32 + lane;
+        int grow;                                                    // weight row of this tile row, -1 = none
+        if (EPI == EPI_SILU_MUL) grow = (r < 64) ? ((n0 + r < p.N) ? n0 + r : -1) : ((n0 + r - 64 < p.N) ? p.up_row_offset + n0 + r - 64 : -1);
+        else grow = (n0 + r < p.N) ? n0 + r : -1;
+        if (grow >= qp.w_rows) grow = -1;
+        const size_t bpr = (size_t)p.K / 256;
+        const uint8_t* wrow = qp.W + (size_t)(grow < 0 ? 0 : grow) * bpr * 144;
+        struct Regs { uint4 h, a, b; };
+        auto load = [&](int i, Regs& x) {
+            if (grow < 0 || i >= nkb) return;
+            const int kb = kb_begin + i;
+            const uint8_t* blk = wrow + (size_t)(kb >> 2) * 144;
+            x.h = __ldg(reinterpret_cast<const uint4*>(blk));
+            x.a = __ldg(reinterpret_cast<const uint4*>(blk + 16 + (kb & 3) * 32));
+            x.b = __ldg(reinterpret_cast<const uint4*>(blk + 32 + (kb & 3) * 32));
+        };
+        bool alive = true;
+        auto produce = [&](int i, const Regs& x) {
+            const int st = i % STAGES;
+            if (alive) {
+                int okw = 1;
+                if (lane == 0) okw = g_mbar_wait(empty0 + 8 * st, ((i / STAGES) & 1) ^ 1, p.err, s_abort) ? 1 : 0;
+                alive = __shfl_sync(0xffffffffu, okw, 0) != 0;
+            }
+            if (!alive) return;
+            unsigned char* brow = tiles_ptr + st * GEMM_STAGE_BYTES + GEMM_BM * GEMM_BK * 2 + r * 128;
+            if (grow < 0) {
+#pragma unroll
+                for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(brow + ((c ^ (r & 7)) << 4)) = make_uint4(0, 0, 0, 0);
+            } else {
+                const int g = (kb_begin + i) & 3;
+                const __half2 dd = *reinterpret_cast<const __half2*>(&x.h.x);
+                const float d = __low2float(dd), dmin = __high2float(dd);
+                float sc0, m0, sc1, m1;
+                q4k_scale_min_u32(x.h.y, x.h.z, x.h.w, 2 * g, sc0, m0);
+                q4k_scale_min_u32(x.h.y, x.h.z, x.h.w, 2 * g + 1, sc1, m1);
+                const float d0 = __fmul_rn(d, sc0), mm0 = __fmul_rn(dmin, m0), d1 = __fmul_rn(d, sc1), mm1 = __fmul_rn(dmin, m1);
+                const uint32_t w[8] = {x.a.x, x.a.y, x.a.z, x.a.w, x.b.x, x.b.y, x.b.z, x.b.w};
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {                   // chunk c = weights 8c..8c+7 of the k-step
+                    const float dx = c < 4 ? d0 : d1, mx = c < 4 ? mm0 : mm1;
+                    uint32_t o[4];
+#pragma unroll
+                    for (int h2 = 0; h2 < 2; ++h2) {
+                        const uint32_t word = w[2 * (c & 3) + h2];
+                        const uint32_t nib = (c < 4 ? word : (word >> 4)) & 0x0F0F0F0Fu;
+                        // nibble -> float without the slow integer conversion: 0x4B0000qq is 2^23 + q exactly
+                        const float f0 = __fsub_rn(__uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7650)), 8388608.0f);
+                        const float f1 = __fsub_rn(__uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7651)), 8388608.0f);
+                        const float f2 = __fsub_rn(__uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7652)), 8388608.0f);
+                        const float f3 = __fsub_rn(__uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7653)), 8388608.0f);
+                        const float v0 = __fsub_rn(__fmul_rn(dx, f0), mx), v1 = __fsub_rn(__fmul_rn(dx, f1), mx);
+                        const float v2 = __fsub_rn(__fmul_rn(dx, f2), mx), v3 = __fsub_rn(__fmul_rn(dx, f3), mx);
+                        const __nv_bfloat162 p0 = __floats2bfloat162_rn(v0, v1), p1 = __floats2bfloat162_rn(v2, v3);
+                        o[2 * h2] = *reinterpret_cast<const uint32_t*>(&p0);
+                        o[2 * h2 + 1] = *reinterpret_cast<const uint32_t*>(&p1);
+                    }
+                    *reinterpret_cast<uint4*>(brow + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");      // generic-proxy writes -> visible to the MMA
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(fullb0 + 8 * st) : "memory");
+        };
+        // two register sets, refilled right after use: a load has two of this group's k-steps to arrive
+        Regs ra = {}, rbuf = {};
+        load(grp, ra);
+        load(grp + 2, rbuf);
+        for (int i = grp; i < nkb; i += 4) {
+            produce(i, ra);
+            load(i + 4, ra);
+            if (i + 2 < nkb) {
+                produce(i + 2, rbuf);
+                load(i + 6, rbuf);
+            }
+        }
+        if (warp < 6) {
+            // ---- epilogue part 1: park the f32 tile column-major in the idle stage buffers ----
+            const int q = warp & 3;
+            const int rloc = q * 32 + lane;
+            const bool ok = __all_sync(0xffffffffu, g_mbar_wait(tfull, 0, p.err, s_abort) && !*s_abort);
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            float* park = reinterpret_cast<float*>(tiles_ptr);
+#pragma unroll
+            for (int c = 0; c < GEMM_BN / 32; ++c) {
+                if (q * 32 >= p.M) break;
+                uint32_t v[32];
+                if (ok) {
+                    tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j) park[(c * 32 + j) * GEMM_BM + rloc] = ok ? __uint_as_float(v[j]) : 0.f;
+            }
+        }
+    }
+    __syncwarp();
+    cluster_sync_all();
+    if (warp >= 2 && !*s_abort) {
+        const uint32_t rank = cluster_ctarank();
+        const int slice = BN_OUT / S;
+        const int rows = min(GEMM_BM, p.M);
+        const uint32_t park_local = tiles;
+        for (int item = (int)threadIdx.x - 64; item < rows * (slice / 8); item += Q4K_THREADS - 64) {
+            const int rr = item % rows, cg = item / rows;
+            const int col = (int)rank * slice + cg * 8;
+            float g[8], u[8], v[GEMM_MAX_SPLIT][8];
+#pragma unroll
+            for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
+                if (peer < S) {
+                    const uint32_t base = map_to_cta(park_local, (uint32_t)peer);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) v[peer][e] = ld_dsmem(base + (uint32_t)(((col + e) * GEMM_BM + rr) * 4));
+                }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) { g[e] = 0.f; u[e] = 0.f; }
+#pragma unroll
+            for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
+                if (peer < S) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) g[e] += v[peer][e];
+                }
+            if (EPI == EPI_SILU_MUL) {
+#pragma unroll
+                for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
+                    if (peer < S) {
+                        const uint32_t base = map_to_cta(park_local, (uint32_t)peer);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) v[peer][e] = ld_dsmem(base + (uint32_t)(((64 + col + e) * GEMM_BM + rr) * 4));
+                    }
+#pragma unroll
+                for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
+                    if (peer < S) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) u[e] += v[peer][e];
+                    }
+            }
+            epilogue_store8<EPI>(p, rr, n0 + col, g, u);
+        }
+    }
+    __syncwarp();
+    cluster_sync_all();
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(128u) : "memory");
+    }
+}
+
 // ---------------------------------------- host side -------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
                                   const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -450,7 +706,58 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
     return QWEN35_OK;
 }
 
+
+// C[M, N] (M <= 128) = epi(A[M, K] . dequant(W)^T), W = Q4_K super-blocks [w_rows][K/256][144]; epi as gemm_bf16
+// (epi 2: gate rows [0, N), up rows [up_row_offset, up_row_offset + N)).  K must be a multiple of 256.
+int gemm_q4k(const bf16* A, int lda, const uint8_t* W, int w_rows, bf16* C, int ldc, const bf16* R, int ldr,
+             int M, int N, int K, int epi, int up_row_offset, cudaStream_t stream) {
+    if (M <= 0 || N <= 0) return QWEN35_OK;
+    if (M > GEMM_BM || K % 256 != 0 || (lda % 8) != 0 || ((uintptr_t)A & 15) || ((uintptr_t)W & 15) || epi < 0 || epi > 2) {
+        set_error("gemm_q4k: needs M <= 128, K a multiple of 256, 16-byte aligned operands, epilogue 0..2");
+        return QWEN35_ERR_BAD_ARG;
+    }
+    void* ws = get_workspace();
+    if (!ws) return QWEN35_ERR_CUDA;
+    CUtensorMap tmA;
+    if (!make_tmap(&tmA, A, M, K, lda, GEMM_BM)) { set_error("cuTensorMapEncodeTiled failed (A %p [%d x %d] ld %d)", (const void*)A, M, K, lda); return QWEN35_ERR_CUDA; }
+    Q4kParams qp{GemmParams{M, N, K, C, ldc, R, ldr, up_row_offset, (int*)ws}, W, w_rows};
+    const int bn_out = (epi == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
+    const int n_tiles = (N + bn_out - 1) / bn_out, nkb = K / GEMM_BK;
+    int split = 1;
+    while (split < GEMM_MAX_SPLIT && n_tiles * split < 120 && nkb / (split * 2) >= 2) split *= 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n_tiles, 1, split);
+    cfg.blockDim = dim3(Q4K_THREADS);
+    cfg.dynamicSmemBytes = Q4K_SMEM;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = (unsigned)split;
+    cfg.attrs = at; cfg.numAttrs = 1;
+#define Q35_GEMM_Q4K(E)                                                                                                            \
+    case E: {                                                                                                                      \
+        static bool attr = false;                                                                                                  \
+        if (!attr) {                                                                                                               \
+            Q35_CUDA_OK(cudaFuncSetAttribute(gemm_q4k_tcgen05_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Q4K_SMEM)); \
+            attr = true;                                                                                                           \
+        }                                                                                                                          \
+        Q35_CUDA_OK(cudaLaunchKernelEx(&cfg, gemm_q4k_tcgen05_kernel<E>, tmA, qp));                                                 \
+        break;                                                                                                                     \
+    }
+    switch (epi) { Q35_GEMM_Q4K(EPI_BF16) Q35_GEMM_Q4K(EPI_RESIDUAL) Q35_GEMM_Q4K(EPI_SILU_MUL) }
+#undef Q35_GEMM_Q4K
+    Q35_CUDA_OK(cudaGetLastError());
+    g_launches.fetch_add(1);
+    return QWEN35_OK;
+}
+
 }  // namespace q35
+
+extern "C" int qwen35_b200_gemm_q4k(const void* A, int lda, const void* W, int w_rows, void* C, int ldc, const void* R, int ldr,
+                                    int M, int N, int K, int epilogue, int up_row_offset, qwen35_stream_t stream) {
+    return q35::gemm_q4k((const q35::bf16*)A, lda, (const uint8_t*)W, w_rows, (q35::bf16*)C, ldc, (const q35::bf16*)R, ldr, M, N, K, epilogue, up_row_offset,
+                         (cudaStream_t)stream);
+}
 
 extern "C" int qwen35_b200_gemm_bf16(const void* A, int lda, const void* B, int b_rows, void* C, int ldc, const void* R, int ldr,
                                      int M, int N, int K, int epilogue, int up_row_offset, qwen35_stream_t stream) {

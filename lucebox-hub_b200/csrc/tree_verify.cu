@@ -9,9 +9,10 @@
 //   DeltaNet         the short conv gathers each node's three predecessors along its parent chain (then the
 //                    committed conv state); the recurrence runs in DFS order, reloads the parent's state when the
 //                    DFS order branches, and persists every node's post-state as f16 for the commit
-// Weights are Q4_K super-blocks (256 weights in 144 bytes).  A linear layer dequantises a row panel of the matrix
-// to bf16 into a scratch panel that stays in L2 (HBM sees the 4.5-bit weights once) and runs the tcgen05 split-K
-// GEMM on the panel; the attention products run on mma.sync tiles with K/V staged through shared memory.
+// Weights are Q4_K super-blocks (256 weights in 144 bytes).  A linear layer is one launch of the tcgen05 split-K
+// GEMM whose weight operand is dequantised by the kernel itself into the swizzled shared-memory tile (HBM sees the
+// 4.5-bit weights once, bf16 weights never exist in global memory); the attention products run on mma.sync tiles
+// with K/V staged through shared memory.
 // Dimensions are run-time values (head_dim 256 and DeltaNet head size 128 are fixed).
 #include <cuda_fp16.h>
 
@@ -24,6 +25,8 @@ namespace q35 {
 
 int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ldc, const bf16* R, int ldr,
               int M, int N, int K, int epi, int up_row_offset, cudaStream_t stream);
+int gemm_q4k(const bf16* A, int lda, const uint8_t* W, int w_rows, bf16* C, int ldc, const bf16* R, int ldr,
+             int M, int N, int K, int epi, int up_row_offset, cudaStream_t stream);
 
 constexpr int TV_MAX_NODES = 40;       // query rows of one kv head (nodes x q-per-kv) must fit shared memory
 constexpr int TV_HD = 256;             // attention head size
@@ -31,7 +34,6 @@ constexpr int TV_DN = 128;             // DeltaNet head size
 constexpr int TV_CHUNK = 128;          // keys per attention CTA
 constexpr int TV_QSTRIDE = TV_HD + 8;  // padded shared-memory row (bf16 elements): conflict-free fragment loads
 constexpr int TV_PSTRIDE = TV_CHUNK + 8;
-constexpr size_t TV_PANEL_BYTES = 48u << 20;   // dequantised bf16 panel, sized to stay in the 126 MB L2
 
 struct TvDims {
     int n_layers, hidden, ffn, vocab, q_heads, kv_heads, head_dim, dn_k_heads, dn_v_heads, dn_dim, rot_dim, fa_period;
@@ -556,7 +558,7 @@ __global__ void tv_commit_kv_kernel(bf16* __restrict__ k_cache, bf16* __restrict
 
 // ------------------------------------------------ host ------------------------------------------------
 struct TvScratch {
-    bf16 *hidden, *resid, *normed, *proj, *ba, *qbuf, *attn, *mlp, *panel, *logits;
+    bf16 *hidden, *resid, *normed, *proj, *ba, *qbuf, *attn, *mlp, *logits;
     float *dn_qkv, *dn_gate, *core, *scores, *stats, *partial;
     int* depth; unsigned long long* anc;
     size_t bytes;
@@ -576,7 +578,7 @@ static TvScratch tv_layout(const TvDims& D, int n, int max_ctx, char* base) {
     s.hidden = (bf16*)take((size_t)n * D.hidden * 2); s.resid = (bf16*)take((size_t)n * D.hidden * 2); s.normed = (bf16*)take((size_t)n * D.hidden * 2);
     s.proj = (bf16*)take((size_t)n * proj_w * 2); s.ba = (bf16*)take((size_t)n * 2 * D.dn_v_heads * 2);
     s.qbuf = (bf16*)take((size_t)n * D.q_heads * TV_HD * 2); s.attn = (bf16*)take((size_t)n * att_w * 2);
-    s.mlp = (bf16*)take((size_t)n * D.ffn * 2); s.panel = (bf16*)take(TV_PANEL_BYTES); s.logits = (bf16*)take((size_t)n * D.vocab * 2);
+    s.mlp = (bf16*)take((size_t)n * D.ffn * 2); s.logits = (bf16*)take((size_t)n * D.vocab * 2);
     s.dn_qkv = (float*)take((size_t)n * conv_ch * 4); s.dn_gate = (float*)take((size_t)n * D.dn_v_heads * 2 * 4);
     s.core = (float*)take((size_t)n * D.dn_v_heads * TV_DN * 4);
     s.scores = (float*)take((size_t)n * D.q_heads * lpad * 4); s.stats = (float*)take((size_t)n * D.q_heads * 2 * 4);
@@ -591,25 +593,10 @@ static bool tv_dims_ok(const TvDims& D) {
            D.rot_dim % 2 == 0 && D.rot_dim <= TV_HD && D.dn_v_heads % D.dn_k_heads == 0 && D.n_layers > 0 && D.fa_period > 0 && D.vocab > 0;
 }
 
-// C[M, out_rows] = epi(X[M, in] . dequant(W[out_rows, in])^T), panel by panel.  epi 2: W = [gate rows ; up rows], out = ffn
+// C[M, out_rows] = epi(X[M, in] . dequant(W[out_rows, in])^T) in one launch.  epi 2: W = [gate rows ; up rows], out = ffn
 static int q4k_linear(const bf16* X, int lda, const uint8_t* W, int out_rows, int in_cols, bf16* C, int ldc, const bf16* R, int ldr,
-                      int M, int epi, bf16* panel, cudaStream_t stream) {
-    const size_t bpr = (size_t)in_cols / 256;                               // super-blocks per weight row
-    const int sets = epi == 2 ? 2 : 1;
-    int pr = (int)(TV_PANEL_BYTES / ((size_t)in_cols * 2 * sets));
-    pr = pr >= 128 ? (pr / 128) * 128 : pr;
-    if (pr <= 0) { set_error("tree_verify: a weight row of %d columns does not fit the dequantisation panel", in_cols); return QWEN35_ERR_BAD_ARG; }
-    for (int r0 = 0; r0 < out_rows; r0 += pr) {
-        const int rows = out_rows - r0 < pr ? out_rows - r0 : pr;
-        const size_t nb = (size_t)rows * bpr;
-        tv_dequant_q4k_kernel<<<(unsigned)((nb + 7) / 8), 256, 0, stream>>>(W, (size_t)r0 * bpr, nb, panel, nullptr);
-        if (epi == 2)
-            tv_dequant_q4k_kernel<<<(unsigned)((nb + 7) / 8), 256, 0, stream>>>(W, ((size_t)out_rows + r0) * bpr, nb, panel + (size_t)rows * in_cols, nullptr);
-        g_launches.fetch_add(sets);
-        const int st = gemm_bf16(X, lda, panel, rows * sets, C + r0, ldc, R ? R + r0 : nullptr, ldr, M, rows, in_cols, epi, rows, stream);
-        if (st != QWEN35_OK) return st;
-    }
-    return QWEN35_OK;
+                      int M, int epi, cudaStream_t stream) {
+    return gemm_q4k(X, lda, W, epi == 2 ? 2 * out_rows : out_rows, C, ldc, R, ldr, M, out_rows, in_cols, epi, out_rows, stream);
 }
 
 }  // namespace q35
@@ -696,7 +683,7 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
         g_launches.fetch_add(1);
         int att_w;
         if (is_fa) {
-            Q35_TRYT(q4k_linear(s.normed, D.hidden, (const uint8_t*)W.w_in, fa_in, D.hidden, s.proj, fa_in, nullptr, 0, n, 0, s.panel, stream));
+            Q35_TRYT(q4k_linear(s.normed, D.hidden, (const uint8_t*)W.w_in, fa_in, D.hidden, s.proj, fa_in, nullptr, 0, n, 0, stream));
             bf16* kc = (bf16*)in->k_cache + (size_t)i_fa * kv_layer;
             bf16* vc = (bf16*)in->v_cache + (size_t)i_fa * kv_layer;
             tv_fa_prep_kernel<<<dim3(n, D.q_heads + 2 * D.kv_heads), 128, 0, stream>>>(s.proj, fa_in, (const float*)W.q_norm, (const float*)W.k_norm, s.depth, D,
@@ -709,7 +696,7 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
             att_w = D.q_heads * TV_HD;
             ++i_fa;
         } else {
-            Q35_TRYT(q4k_linear(s.normed, D.hidden, (const uint8_t*)W.w_in, dn_in, D.hidden, s.proj, dn_in, nullptr, 0, n, 0, s.panel, stream));
+            Q35_TRYT(q4k_linear(s.normed, D.hidden, (const uint8_t*)W.w_in, dn_in, D.hidden, s.proj, dn_in, nullptr, 0, n, 0, stream));
             Q35_TRYT(gemm_bf16(s.normed, D.hidden, (const bf16*)W.w_ba, 2 * D.dn_v_heads, s.ba, 2 * D.dn_v_heads, nullptr, 0, n, 2 * D.dn_v_heads, D.hidden, 0, 0, stream));
             float* cstate = (float*)in->conv_state + (size_t)i_dn * 3 * conv_ch;
             float* nconv = (float*)in->node_conv + (size_t)i_dn * nconv_layer;
@@ -723,16 +710,16 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
             att_w = D.dn_v_heads * TV_DN;
             ++i_dn;
         }
-        Q35_TRYT(q4k_linear(s.attn, att_w, (const uint8_t*)W.w_out, D.hidden, att_w, s.resid, D.hidden, s.hidden, D.hidden, n, 1, s.panel, stream));
+        Q35_TRYT(q4k_linear(s.attn, att_w, (const uint8_t*)W.w_out, D.hidden, att_w, s.resid, D.hidden, s.hidden, D.hidden, n, 1, stream));
         tv_rmsnorm_kernel<<<n, 256, 0, stream>>>(s.resid, (const float*)W.post_norm, s.normed, D.hidden, D.eps);
         g_launches.fetch_add(1);
-        Q35_TRYT(q4k_linear(s.normed, D.hidden, (const uint8_t*)W.w_gate_up, D.ffn, D.hidden, s.mlp, D.ffn, nullptr, 0, n, 2, s.panel, stream));
-        Q35_TRYT(q4k_linear(s.mlp, D.ffn, (const uint8_t*)W.w_down, D.hidden, D.ffn, s.hidden, D.hidden, s.resid, D.hidden, n, 1, s.panel, stream));
+        Q35_TRYT(q4k_linear(s.normed, D.hidden, (const uint8_t*)W.w_gate_up, D.ffn, D.hidden, s.mlp, D.ffn, nullptr, 0, n, 2, stream));
+        Q35_TRYT(q4k_linear(s.mlp, D.ffn, (const uint8_t*)W.w_down, D.hidden, D.ffn, s.hidden, D.hidden, s.resid, D.hidden, n, 1, stream));
         if (in->dbg_hidden)
             Q35_CUDA_OK(cudaMemcpyAsync((bf16*)in->dbg_hidden + (size_t)il * n * D.hidden, s.hidden, (size_t)n * D.hidden * 2, cudaMemcpyDeviceToDevice, stream));
     }
     tv_rmsnorm_kernel<<<n, 256, 0, stream>>>(s.hidden, (const float*)in->output_norm, s.normed, D.hidden, D.eps);
-    Q35_TRYT(q4k_linear(s.normed, D.hidden, (const uint8_t*)in->output_w, D.vocab, D.hidden, s.logits, D.vocab, nullptr, 0, n, 0, s.panel, stream));
+    Q35_TRYT(q4k_linear(s.normed, D.hidden, (const uint8_t*)in->output_w, D.vocab, D.hidden, s.logits, D.vocab, nullptr, 0, n, 0, stream));
     tv_argmax_kernel<<<n, 1024, 0, stream>>>(s.logits, D.vocab, in->node_argmax);
     g_launches.fetch_add(2);
     if (in->logits_out) Q35_CUDA_OK(cudaMemcpyAsync(in->logits_out, s.logits, (size_t)n * D.vocab * 2, cudaMemcpyDeviceToDevice, stream));

@@ -103,6 +103,7 @@ SIGNATURES = {
     "qwen35_b200_tree_commit": (_i, [C.POINTER(TreeVerifyArgs), _vp, _vp, _vp]),
     "qwen35_b200_dequant_q4k": (_i, [_vp, C.c_size_t, _vp, _vp, _vp]),
     "qwen35_b200_gemm_bf16": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "qwen35_b200_gemm_q4k": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "qwen35_b200_status": (_i, [_vp]),
     "qwen35_b200_clear_status": (_i, [_vp]),
     "qwen35_b200_debug_read": (_i, [_i, _vp]),

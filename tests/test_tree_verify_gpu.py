@@ -33,6 +33,41 @@ def test_q4k_dequant_gpu_bit_exact():
     assert torch.equal(got16.view(torch.int16), ref.bfloat16().view(torch.int16))
 
 
+@pytest.mark.parametrize("M,N,K,epi", [(33, 512, 512, 0), (7, 1000, 1024, 0), (40, 2048, 5120, 1), (33, 1024, 17408, 1), (33, 3584, 1024, 2),
+                                       (1, 128, 256, 0), (128, 640, 768, 2)])
+def test_q4k_gemm_matches_dequantised_reference(M, N, K, epi):
+    """Fused dequantisation GEMM against torch on the dequantised (bf16-rounded) weights: same values, f32 sums in a
+    different order, so a few outputs may land one bf16 step away."""
+    import ctypes as C
+    from oracle.tree_verify_oracle import q4k_dequant
+    from qwen35_b200 import _capi
+    from qwen35_b200.tree_verify import random_q4k
+    torch.manual_seed(M + N)
+    rows = 2 * N if epi == 2 else N
+    blocks = random_q4k(rows, K, 17 + N, sigma=0.05)
+    W = torch.from_numpy(q4k_dequant(blocks.numpy().reshape(-1, 144))).reshape(rows, K).bfloat16().float().cuda()
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    R = torch.randn(M, N, device="cuda").bfloat16()
+    out = torch.zeros(M, N, dtype=torch.bfloat16, device="cuda")
+    lib = _capi.lib()
+    bq = blocks.cuda()
+    _capi.check(lib.qwen35_b200_gemm_q4k(A.data_ptr(), K, bq.data_ptr(), rows, out.data_ptr(), N, R.data_ptr(), N, M, N, K, epi, N,
+                                         C.c_void_p(torch.cuda.current_stream().cuda_stream)), "gemm_q4k")
+    _capi.check(lib.qwen35_b200_status(None), "status")
+    acc = A.float() @ W.t()
+    if epi == 0:
+        ref = acc.bfloat16()
+    elif epi == 1:
+        ref = (acc.bfloat16().float() + R.float()).bfloat16()
+    else:
+        g, u = acc[:, :N].bfloat16().float(), acc[:, N:].bfloat16().float()
+        ref = ((g * torch.sigmoid(g)).bfloat16().float() * u).bfloat16()
+    diff = (out.float() - ref.float()).abs()
+    assert float((out != ref).float().mean()) <= 0.02
+    # one bf16 step of the rounded accumulator (the residual add can cancel, so the bound follows |acc|, not |result|)
+    assert bool((diff <= (acc[:, :N].abs() + ref.float().abs()) * 2.0 ** -6 + 2e-3).all())
+
+
 def _setup(n_ctx, seed):
     from oracle.tree_verify_oracle import TreeOracle
     from qwen35_b200.tree_verify import TreeTarget, make_random_tree_weights
