@@ -337,17 +337,28 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
 }
 
 // ------------------------------------------------------------------------------------------------------------
-// Q4_K weights: C[M <= 128, N] = epi(A[M, K] . dequant(W[N, K])^T).  Same pipeline as the split-K kernel above, but
-// the weight operand never exists in global memory as bf16: eight dequantisation warps read the 4.5-bit super-blocks
-// and write bf16(value) straight into the 128-byte-swizzled shared-memory tile the MMA descriptor expects.
-// A 64-wide k-step of one weight row is exactly one 64-weight group of a Q4_K super-block (32 nibble bytes, two
-// 6-bit scale/min pairs), so one thread dequantises one tile row per k-step: 2 x 16-byte loads + the 16-byte header.
-//   warp 0      TMA producer of the activation tile        warp 1   MMA issue (waits for both operands of a stage)
-//   warps 2-5   dequantise even k-steps, then the epilogue  warps 6-9 dequantise odd k-steps
+// Q4_K weights: C[M <= 64, N] = epi(A[M, K] . dequant(W[N, K])^T).  Same split-K cluster scheme as above, but the
+// weight operand never exists in global memory as bf16:
+//   warp 0      TMA producer: activation tiles (two 64-wide slabs per 128-wide k-step) and RAW Q4_K super-blocks,
+//               one box of 144 bytes x 64 rows per half tile (a whole super-block row per request: HBM sees
+//               contiguous 144-byte pieces, never 16- or 32-byte ones)
+//   warps 2-9   dequantise from the raw ring into the 128-byte-swizzled bf16 tile the MMA descriptor expects:
+//               a 64-weight group of a super-block is exactly one 64-wide slab row, so thread (row, h) converts
+//               group h of the k-step for one tile row (3 conflict-free 16-byte shared loads, 8 swizzled stores)
+//   warp 1      MMA issue: 8 x (M128 N128 K16) per k-step once both operands of the stage are there
+//   warps 2-5   epilogue afterwards (park, cluster reduce, store) as in the bf16 kernel
+// The activation box holds 64 rows; the MMA reads 128, so accumulator rows 64-127 are garbage and are never read.
+// ncu on the gate/up shape (33 x 17408 x 5120): tensor pipe 10 % active, issue slots 61 % busy, 10 instructions per
+// weight: the kernel is bound by the dequantisation arithmetic, not by HBM (13 %) or the MMA.
 // value = bf16((d*sc)*q - dmin*m) with separate f32 roundings, the published Q4_K dequantisation.
-constexpr int Q4K_THREADS = 320;
-constexpr int Q4K_STAGES = 3;
-constexpr uint32_t Q4K_SMEM = Q4K_STAGES * GEMM_STAGE_BYTES + 1024 + 256;
+constexpr int Q4K_THREADS = 576;                                                      // 2 + 16 dequantisation warps
+constexpr int Q4K_DQ_WARPS = 16;
+constexpr int Q4K_STAGES = 3, Q4K_RAW_STAGES = 3;
+constexpr uint32_t Q4K_A_SLAB = 64 * 128, Q4K_B_SLAB = 128 * 128;                      // bytes
+constexpr uint32_t Q4K_STAGE_BYTES = 2 * Q4K_A_SLAB + 2 * Q4K_B_SLAB;                 // 48 KB per 128-wide k-step
+constexpr uint32_t Q4K_RAW_BYTES = 128 * 144;                                          // one super-block per tile row
+constexpr uint32_t Q4K_SMEM = Q4K_STAGES * Q4K_STAGE_BYTES + Q4K_RAW_STAGES * Q4K_RAW_BYTES + 1024 + 256;
+static_assert(Q4K_STAGES * Q4K_STAGE_BYTES >= GEMM_BM * GEMM_BN * 4, "the parked f32 tile reuses the stage buffers");
 
 __device__ __forceinline__ void q4k_scale_min_u32(uint32_t s0, uint32_t s1, uint32_t s2, int j, float& sc, float& mn) {
     // s0, s1, s2 = scale bytes 0-3, 4-7, 8-11
@@ -362,38 +373,36 @@ __device__ __forceinline__ void q4k_scale_min_u32(uint32_t s0, uint32_t s1, uint
     }
 }
 
-struct Q4kParams {
-    GemmParams g;
-    const uint8_t* W;       // super-blocks, row-major [rows][K/256][144]
-    int w_rows;             // rows that exist in W (rows beyond read as zero)
-};
-
 template <int EPI>
-__global__ void __launch_bounds__(Q4K_THREADS, 2)
-gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const Q4kParams qp) {
-    const GemmParams& p = qp.g;
-    constexpr int STAGES = Q4K_STAGES;
+__global__ void __launch_bounds__(Q4K_THREADS, 1)
+gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW, const GemmParams p) {
+    constexpr int STAGES = Q4K_STAGES, RS = Q4K_RAW_STAGES;
     extern __shared__ unsigned char g_smem_raw[];
     const uint32_t raw = g_smem_u32(g_smem_raw);
     const uint32_t tiles = (raw + 1023u) & ~1023u;
     unsigned char* tiles_ptr = g_smem_raw + (tiles - raw);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(tiles_ptr + STAGES * GEMM_STAGE_BYTES);
-    const uint32_t fulla0 = g_smem_u32(bars), fullb0 = fulla0 + 8 * STAGES, empty0 = fullb0 + 8 * STAGES, tfull = empty0 + 8 * STAGES;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 1);
+    unsigned char* rawring_ptr = tiles_ptr + STAGES * Q4K_STAGE_BYTES;
+    const uint32_t rawring = tiles + STAGES * Q4K_STAGE_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(rawring_ptr + RS * Q4K_RAW_BYTES);
+    const uint32_t fulla0 = g_smem_u32(bars), fullb0 = fulla0 + 8 * STAGES, empty0 = fullb0 + 8 * STAGES, fullr0 = empty0 + 8 * STAGES,
+                   emptyr0 = fullr0 + 8 * RS, tfull = emptyr0 + 8 * RS;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 2 * RS + 1);
     volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int BN_OUT = (EPI == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
     const int n0 = blockIdx.x * BN_OUT;
-    const int nkb_all = p.K / GEMM_BK;
+    const int sb_all = p.K / 256;
     const int S = (int)gridDim.z, z = (int)blockIdx.z;
-    const int kb_begin = (int)(((long long)z * nkb_all) / S), kb_end = (int)(((long long)(z + 1) * nkb_all) / S);
-    const int nkb = kb_end - kb_begin;
+    const int sb_begin = (int)(((long long)z * sb_all) / S), sb_end = (int)(((long long)(z + 1) * sb_all) / S);
+    const int nk2 = 2 * (sb_end - sb_begin);                 // 128-wide k-steps of this CTA (two per super-block)
 
     if (threadIdx.x == 0) {
         asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmW) : "memory");
         *s_abort = 0;
-        for (int i = 0; i < STAGES; ++i) { g_mbar_init(fulla0 + 8 * i, 1); g_mbar_init(fullb0 + 8 * i, 4); g_mbar_init(empty0 + 8 * i, 1); }
+        for (int i = 0; i < STAGES; ++i) { g_mbar_init(fulla0 + 8 * i, 1); g_mbar_init(fullb0 + 8 * i, Q4K_DQ_WARPS); g_mbar_init(empty0 + 8 * i, 1); }
+        for (int i = 0; i < RS; ++i) { g_mbar_init(fullr0 + 8 * i, 1); g_mbar_init(emptyr0 + 8 * i, Q4K_DQ_WARPS); }
         g_mbar_init(tfull, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -408,113 +417,108 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const Q4kParams
 
     if (warp == 0) {
         if (lane == 0) {
-            int issued = 0;
-            for (int i = 0; i < nkb; ++i) {
+            int issued_a = 0, issued_r = 0;
+            for (int i = 0; i < nk2; ++i) {
+                if ((i & 1) == 0) {
+                    const int j = i >> 1, rs = j % RS;
+                    if (!g_mbar_wait(emptyr0 + 8 * rs, ((j / RS) & 1) ^ 1, p.err, s_abort)) break;
+                    g_mbar_expect_tx(fullr0 + 8 * rs, Q4K_RAW_BYTES);
+                    const uint32_t dst = rawring + rs * Q4K_RAW_BYTES;
+                    g_tma_load_2d(dst, &tmW, (sb_begin + j) * 144, n0, fullr0 + 8 * rs);
+                    g_tma_load_2d(dst + 64 * 144, &tmW, (sb_begin + j) * 144, (EPI == EPI_SILU_MUL ? p.up_row_offset : 64) + n0, fullr0 + 8 * rs);
+                    issued_r = j + 1;
+                }
                 const int st = i % STAGES;
                 if (!g_mbar_wait(empty0 + 8 * st, ((i / STAGES) & 1) ^ 1, p.err, s_abort)) break;
-                g_mbar_expect_tx(fulla0 + 8 * st, GEMM_BM * GEMM_BK * 2);
-                g_tma_load_2d(tiles + st * GEMM_STAGE_BYTES, &tmA, (kb_begin + i) * GEMM_BK, 0, fulla0 + 8 * st);
-                issued = i + 1;
+                g_mbar_expect_tx(fulla0 + 8 * st, 2 * Q4K_A_SLAB);
+                const uint32_t a_dst = tiles + st * Q4K_STAGE_BYTES;
+                const int kcol = (sb_begin * 2 + i) * 128;
+                g_tma_load_2d(a_dst, &tmA, kcol, 0, fulla0 + 8 * st);
+                g_tma_load_2d(a_dst + Q4K_A_SLAB, &tmA, kcol + 64, 0, fulla0 + 8 * st);
+                issued_a = i + 1;
             }
-            if (*s_abort) {
-                for (int i = max(0, issued - STAGES); i < issued; ++i) {
+            if (*s_abort) {      // copies in flight must land before the CTA may exit
+                for (int i = max(0, issued_a - STAGES); i < issued_a; ++i) {
                     unsigned it = 0;
                     while (!g_mbar_try_wait(fulla0 + 8 * (i % STAGES), (i / STAGES) & 1) && ++it < GEMM_SPIN_LIMIT) {}
+                }
+                for (int j = max(0, issued_r - RS); j < issued_r; ++j) {
+                    unsigned it = 0;
+                    while (!g_mbar_try_wait(fullr0 + 8 * (j % RS), (j / RS) & 1) && ++it < GEMM_SPIN_LIMIT) {}
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            for (int i = 0; i < nkb; ++i) {
+            for (int i = 0; i < nk2; ++i) {
                 const int st = i % STAGES;
                 if (!g_mbar_wait(fulla0 + 8 * st, (i / STAGES) & 1, p.err, s_abort)) break;
                 if (!g_mbar_wait(fullb0 + 8 * st, (i / STAGES) & 1, p.err, s_abort)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t a_addr = tiles + st * GEMM_STAGE_BYTES, b_addr = a_addr + GEMM_BM * GEMM_BK * 2;
-                const uint64_t adesc = make_smem_desc(a_addr), bdesc = make_smem_desc(b_addr);
+                const uint32_t a_addr = tiles + st * Q4K_STAGE_BYTES, b_addr = a_addr + 2 * Q4K_A_SLAB;
 #pragma unroll
-                for (int k = 0; k < GEMM_BK / 16; ++k)
-                    umma_bf16(tmem_base, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), GEMM_IDESC, (i > 0 || k > 0) ? 1u : 0u);
+                for (int sl = 0; sl < 2; ++sl) {
+                    const uint64_t adesc = make_smem_desc(a_addr + sl * Q4K_A_SLAB), bdesc = make_smem_desc(b_addr + sl * Q4K_B_SLAB);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        umma_bf16(tmem_base, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), GEMM_IDESC, (i > 0 || sl > 0 || k > 0) ? 1u : 0u);
+                }
                 umma_commit(empty0 + 8 * st);
             }
             umma_commit(tfull);
         }
     } else {
-        // ---- dequantisation: group 0 (warps 2-5) even k-steps, group 1 (warps 6-9) odd k-steps; thread = tile row ----
-        const int grp = (warp - 2) >> 2, r = ((warp - 2) & 3) * 32 + lane;
-        int grow;                                                    // weight row of this tile row, -1 = none
-        if (EPI == EPI_SILU_MUL) grow = (r < 64) ? ((n0 + r < p.N) ? n0 + r : -1) : ((n0 + r - 64 < p.N) ? p.up_row_offset + n0 + r - 64 : -1);
-        else grow = (n0 + r < p.N) ? n0 + r : -1;
-        if (grow >= qp.w_rows) grow = -1;
-        const size_t bpr = (size_t)p.K / 256;
-        const uint8_t* wrow = qp.W + (size_t)(grow < 0 ? 0 : grow) * bpr * 144;
-        struct Regs { uint4 h, a, b; };
-        auto load = [&](int i, Regs& x) {
-            if (grow < 0 || i >= nkb) return;
-            const int kb = kb_begin + i;
-            const uint8_t* blk = wrow + (size_t)(kb >> 2) * 144;
-            x.h = __ldg(reinterpret_cast<const uint4*>(blk));
-            x.a = __ldg(reinterpret_cast<const uint4*>(blk + 16 + (kb & 3) * 32));
-            x.b = __ldg(reinterpret_cast<const uint4*>(blk + 32 + (kb & 3) * 32));
-        };
+        // ---- dequantisation: thread (row, h, part) converts half of group h (16 nibble bytes = 32 weights: chunks
+        // 2*part, 2*part+1 from the low nibbles, 4+2*part, 5+2*part from the high ones) of every k-step ----
+        const int dw = warp - 2, row = (dw & 3) * 32 + lane, h = (dw >> 2) & 1, part = dw >> 3;
         bool alive = true;
-        auto produce = [&](int i, const Regs& x) {
-            const int st = i % STAGES;
-            if (alive) {
-                int okw = 1;
-                if (lane == 0) okw = g_mbar_wait(empty0 + 8 * st, ((i / STAGES) & 1) ^ 1, p.err, s_abort) ? 1 : 0;
-                alive = __shfl_sync(0xffffffffu, okw, 0) != 0;
-            }
-            if (!alive) return;
-            unsigned char* brow = tiles_ptr + st * GEMM_STAGE_BYTES + GEMM_BM * GEMM_BK * 2 + r * 128;
-            if (grow < 0) {
+        for (int i = 0; i < nk2 && alive; ++i) {
+            const int st = i % STAGES, j = i >> 1, rs = j % RS;
+            int okw = 1;
+            if (lane == 0)
+                okw = (g_mbar_wait(fullr0 + 8 * rs, (j / RS) & 1, p.err, s_abort) && g_mbar_wait(empty0 + 8 * st, ((i / STAGES) & 1) ^ 1, p.err, s_abort)) ? 1 : 0;
+            alive = __shfl_sync(0xffffffffu, okw, 0) != 0;
+            if (!alive) break;
+            const unsigned char* rb = rawring_ptr + rs * Q4K_RAW_BYTES + row * 144;
+            const int g = 2 * (i & 1) + h;
+            const uint4 hd = *reinterpret_cast<const uint4*>(rb);
+            const uint4 qv = *reinterpret_cast<const uint4*>(rb + 16 + 32 * g + 16 * part);
+            const __half2 dd = *reinterpret_cast<const __half2*>(&hd.x);
+            const float d = __low2float(dd), dmin = __high2float(dd);
+            float sc0, m0, sc1, m1;
+            q4k_scale_min_u32(hd.y, hd.z, hd.w, 2 * g, sc0, m0);
+            q4k_scale_min_u32(hd.y, hd.z, hd.w, 2 * g + 1, sc1, m1);
+            const float d0 = __fmul_rn(d, sc0), mm0 = __fmul_rn(dmin, m0), d1 = __fmul_rn(d, sc1), mm1 = __fmul_rn(dmin, m1);
+            const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
+            unsigned char* brow = tiles_ptr + st * Q4K_STAGE_BYTES + 2 * Q4K_A_SLAB + h * Q4K_B_SLAB + row * 128;
 #pragma unroll
-                for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(brow + ((c ^ (r & 7)) << 4)) = make_uint4(0, 0, 0, 0);
-            } else {
-                const int g = (kb_begin + i) & 3;
-                const __half2 dd = *reinterpret_cast<const __half2*>(&x.h.x);
-                const float d = __low2float(dd), dmin = __high2float(dd);
-                float sc0, m0, sc1, m1;
-                q4k_scale_min_u32(x.h.y, x.h.z, x.h.w, 2 * g, sc0, m0);
-                q4k_scale_min_u32(x.h.y, x.h.z, x.h.w, 2 * g + 1, sc1, m1);
-                const float d0 = __fmul_rn(d, sc0), mm0 = __fmul_rn(dmin, m0), d1 = __fmul_rn(d, sc1), mm1 = __fmul_rn(dmin, m1);
-                const uint32_t w[8] = {x.a.x, x.a.y, x.a.z, x.a.w, x.b.x, x.b.y, x.b.z, x.b.w};
+            for (int cc = 0; cc < 4; ++cc) {                    // cc 0,1: low nibbles; 2,3: high nibbles
+                const bool hi = cc >= 2;
+                const int c = (hi ? 4 : 0) + 2 * part + (cc & 1);     // chunk = weights 8c..8c+7 of the group
+                const float dx = hi ? d1 : d0, mx = hi ? mm1 : mm0;
+                uint32_t o[4];
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {                   // chunk c = weights 8c..8c+7 of the k-step
-                    const float dx = c < 4 ? d0 : d1, mx = c < 4 ? mm0 : mm1;
-                    uint32_t o[4];
-#pragma unroll
-                    for (int h2 = 0; h2 < 2; ++h2) {
-                        const uint32_t word = w[2 * (c & 3) + h2];
-                        const uint32_t nib = (c < 4 ? word : (word >> 4)) & 0x0F0F0F0Fu;
-                        // nibble -> float without the slow integer conversion: 0x4B0000qq is 2^23 + q exactly
-                        const float f0 = __fsub_rn(__uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7650)), 8388608.0f);
-                        const float f1 = __fsub_rn(__uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7651)), 8388608.0f);
-                        const float f2 = __fsub_rn(__uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7652)), 8388608.0f);
-                        const float f3 = __fsub_rn(__uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7653)), 8388608.0f);
-                        const float v0 = __fsub_rn(__fmul_rn(dx, f0), mx), v1 = __fsub_rn(__fmul_rn(dx, f1), mx);
-                        const float v2 = __fsub_rn(__fmul_rn(dx, f2), mx), v3 = __fsub_rn(__fmul_rn(dx, f3), mx);
-                        const __nv_bfloat162 p0 = __floats2bfloat162_rn(v0, v1), p1 = __floats2bfloat162_rn(v2, v3);
-                        o[2 * h2] = *reinterpret_cast<const uint32_t*>(&p0);
-                        o[2 * h2 + 1] = *reinterpret_cast<const uint32_t*>(&p1);
-                    }
-                    *reinterpret_cast<uint4*>(brow + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                for (int h2 = 0; h2 < 2; ++h2) {
+                    const uint32_t word = w[2 * (cc & 1) + h2];
+                    const uint32_t nib = (hi ? (word >> 4) : word) & 0x0F0F0F0Fu;
+                    // nibble -> float without the slow integer conversion: 0x4B0000qq is 2^23 + q exactly
+                    const float f0 = __fsub_rn(__uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7650)), 8388608.0f);
+                    const float f1 = __fsub_rn(__uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7651)), 8388608.0f);
+                    const float f2 = __fsub_rn(__uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7652)), 8388608.0f);
+                    const float f3 = __fsub_rn(__uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7653)), 8388608.0f);
+                    const float v0 = __fsub_rn(__fmul_rn(dx, f0), mx), v1 = __fsub_rn(__fmul_rn(dx, f1), mx);
+                    const float v2 = __fsub_rn(__fmul_rn(dx, f2), mx), v3 = __fsub_rn(__fmul_rn(dx, f3), mx);
+                    const __nv_bfloat162 p0 = __floats2bfloat162_rn(v0, v1), p1 = __floats2bfloat162_rn(v2, v3);
+                    o[2 * h2] = *reinterpret_cast<const uint32_t*>(&p0);
+                    o[2 * h2 + 1] = *reinterpret_cast<const uint32_t*>(&p1);
                 }
+                *reinterpret_cast<uint4*>(brow + ((c ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");      // generic-proxy writes -> visible to the MMA
             __syncwarp();
-            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(fullb0 + 8 * st) : "memory");
-        };
-        // two register sets, refilled right after use: a load has two of this group's k-steps to arrive
-        Regs ra = {}, rbuf = {};
-        load(grp, ra);
-        load(grp + 2, rbuf);
-        for (int i = grp; i < nkb; i += 4) {
-            produce(i, ra);
-            load(i + 4, ra);
-            if (i + 2 < nkb) {
-                produce(i + 2, rbuf);
-                load(i + 6, rbuf);
+            if (lane == 0) {
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(fullb0 + 8 * st) : "memory");
+                if (i & 1) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(emptyr0 + 8 * rs) : "memory");   // super-block consumed
             }
         }
         if (warp < 6) {
@@ -523,10 +527,10 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const Q4kParams
             const int rloc = q * 32 + lane;
             const bool ok = __all_sync(0xffffffffu, g_mbar_wait(tfull, 0, p.err, s_abort) && !*s_abort);
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            float* park = reinterpret_cast<float*>(tiles_ptr);
+            float* park = reinterpret_cast<float*>(tiles_ptr);          // [weight column of the tile][activation row]
 #pragma unroll
             for (int c = 0; c < GEMM_BN / 32; ++c) {
-                if (q * 32 >= p.M) break;
+                if (q * 32 >= p.M) break;                               // rows of this warp are never read back
                 uint32_t v[32];
                 if (ok) {
                     tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
@@ -542,7 +546,7 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const Q4kParams
     if (warp >= 2 && !*s_abort) {
         const uint32_t rank = cluster_ctarank();
         const int slice = BN_OUT / S;
-        const int rows = min(GEMM_BM, p.M);
+        const int rows = min(64, p.M);
         const uint32_t park_local = tiles;
         for (int item = (int)threadIdx.x - 64; item < rows * (slice / 8); item += Q4K_THREADS - 64) {
             const int rr = item % rows, cg = item / rows;
@@ -617,6 +621,20 @@ static bool make_tmap(CUtensorMap* tm, const void* ptr, int rows, int cols, int 
     cuuint32_t estr[2] = {1, 1};
     return fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Q4_K super-blocks as a 2-D byte tensor [rows][K/256 * 144]; box = one super-block (144 bytes) x 64 rows, no swizzle.
+static bool make_tmap_q4k(CUtensorMap* tm, const void* ptr, int rows, int K) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t row_bytes = (cuuint64_t)(K / 256) * 144;
+    cuuint64_t dims[2] = {row_bytes, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {144, 64};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -707,24 +725,27 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
 }
 
 
-// C[M, N] (M <= 128) = epi(A[M, K] . dequant(W)^T), W = Q4_K super-blocks [w_rows][K/256][144]; epi as gemm_bf16
+// C[M, N] (M <= 64) = epi(A[M, K] . dequant(W)^T), W = Q4_K super-blocks [w_rows][K/256][144]; epi as gemm_bf16
 // (epi 2: gate rows [0, N), up rows [up_row_offset, up_row_offset + N)).  K must be a multiple of 256.
 int gemm_q4k(const bf16* A, int lda, const uint8_t* W, int w_rows, bf16* C, int ldc, const bf16* R, int ldr,
              int M, int N, int K, int epi, int up_row_offset, cudaStream_t stream) {
     if (M <= 0 || N <= 0) return QWEN35_OK;
-    if (M > GEMM_BM || K % 256 != 0 || (lda % 8) != 0 || ((uintptr_t)A & 15) || ((uintptr_t)W & 15) || epi < 0 || epi > 2) {
-        set_error("gemm_q4k: needs M <= 128, K a multiple of 256, 16-byte aligned operands, epilogue 0..2");
+    if (M > 64 || K % 256 != 0 || (lda % 8) != 0 || ((uintptr_t)A & 15) || ((uintptr_t)W & 15) || epi < 0 || epi > 2) {
+        set_error("gemm_q4k: needs M <= 64, K a multiple of 256, 16-byte aligned operands, epilogue 0..2");
         return QWEN35_ERR_BAD_ARG;
     }
     void* ws = get_workspace();
     if (!ws) return QWEN35_ERR_CUDA;
-    CUtensorMap tmA;
-    if (!make_tmap(&tmA, A, M, K, lda, GEMM_BM)) { set_error("cuTensorMapEncodeTiled failed (A %p [%d x %d] ld %d)", (const void*)A, M, K, lda); return QWEN35_ERR_CUDA; }
-    Q4kParams qp{GemmParams{M, N, K, C, ldc, R, ldr, up_row_offset, (int*)ws}, W, w_rows};
+    CUtensorMap tmA, tmW;
+    if (!make_tmap(&tmA, A, M, K, lda, 64) || !make_tmap_q4k(&tmW, W, w_rows, K)) {
+        set_error("cuTensorMapEncodeTiled failed (A %p [%d x %d] ld %d; W %p [%d rows])", (const void*)A, M, K, lda, (const void*)W, w_rows);
+        return QWEN35_ERR_CUDA;
+    }
+    GemmParams qp{M, N, K, C, ldc, R, ldr, up_row_offset, (int*)ws};
     const int bn_out = (epi == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
-    const int n_tiles = (N + bn_out - 1) / bn_out, nkb = K / GEMM_BK;
+    const int n_tiles = (N + bn_out - 1) / bn_out, nsb = K / 256;
     int split = 1;
-    while (split < GEMM_MAX_SPLIT && n_tiles * split < 120 && nkb / (split * 2) >= 2) split *= 2;
+    while (split < GEMM_MAX_SPLIT && n_tiles * split < 120 && nsb / (split * 2) >= 2) split *= 2;      // >= 2 super-blocks per CTA
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(n_tiles, 1, split);
     cfg.blockDim = dim3(Q4K_THREADS);
@@ -741,7 +762,7 @@ int gemm_q4k(const bf16* A, int lda, const uint8_t* W, int w_rows, bf16* C, int 
             Q35_CUDA_OK(cudaFuncSetAttribute(gemm_q4k_tcgen05_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Q4K_SMEM)); \
             attr = true;                                                                                                           \
         }                                                                                                                          \
-        Q35_CUDA_OK(cudaLaunchKernelEx(&cfg, gemm_q4k_tcgen05_kernel<E>, tmA, qp));                                                 \
+        Q35_CUDA_OK(cudaLaunchKernelEx(&cfg, gemm_q4k_tcgen05_kernel<E>, tmA, tmW, qp));                                                 \
         break;                                                                                                                     \
     }
     switch (epi) { Q35_GEMM_Q4K(EPI_BF16) Q35_GEMM_Q4K(EPI_RESIDUAL) Q35_GEMM_Q4K(EPI_SILU_MUL) }
