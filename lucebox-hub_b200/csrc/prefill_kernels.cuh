@@ -433,6 +433,161 @@ static __global__ void __launch_bounds__(ATT_PF_WARPS * 32) pf_attention_kernel(
     *(reinterpret_cast<uint4*>(out + (size_t)t * FA_Q_SIZE + head * FA_HEAD_DIM) + lane) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// ---- causal GQA attention on tensor cores (mma.sync m16n8k16 bf16), same rounding points as above -----------
+// One CTA = 32 queries x the 4 q heads of one kv head = 128 rows (row r: query r/4, head r%4), one 16-row tile per
+// warp, so a K/V chunk staged in shared memory serves all four heads.  Exact softmax in two passes over the causal
+// key range: pass 1 the running row maximum and normaliser from bf16(q.k)/16; pass 2 recomputes the same scores (same
+// instructions, same values), forms P = bf16(exp(s - m) / l) in registers (the accumulator layout of two adjacent
+// 8-key tiles is the A-operand layout of a 16-key step) and accumulates P.V.  Fragments come from ldmatrix on rows
+// padded to 528 bytes (conflict-free); V is read with ldmatrix.trans.
+constexpr int ATT_MMA_Q = 32, ATT_MMA_ROWS = ATT_MMA_Q * FA_GQA, ATT_MMA_KEYS = 64, ATT_MMA_LD = FA_HEAD_DIM + 8;
+constexpr int ATT_MMA_SMEM = (ATT_MMA_ROWS + 2 * ATT_MMA_KEYS) * ATT_MMA_LD * 2;
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+    const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];" : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* p) {
+    const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];" : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+static __global__ void __launch_bounds__(256, 1) pf_attention_mma_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k_cache,
+                                                                  const bf16* __restrict__ v_cache, const bf16* __restrict__ proj, int ldp,
+                                                                  bf16* __restrict__ out, int S, int max_seq) {
+    extern __shared__ __align__(16) unsigned char att_mma_sm[];
+    bf16* Qs = reinterpret_cast<bf16*>(att_mma_sm);
+    bf16* Ks = Qs + ATT_MMA_ROWS * ATT_MMA_LD;
+    bf16* Vs = Ks + ATT_MMA_KEYS * ATT_MMA_LD;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+    const int blk = (int)gridDim.x - 1 - (int)blockIdx.x;          // long blocks first
+    const int kvh = blockIdx.y, q0 = blk * ATT_MMA_Q;
+    const bf16* kb = k_cache + (size_t)kvh * max_seq * FA_HEAD_DIM;
+    const bf16* vb = v_cache + (size_t)kvh * max_seq * FA_HEAD_DIM;
+    for (int i = tid; i < ATT_MMA_ROWS * (FA_HEAD_DIM / 8); i += 256) {
+        const int r = i / (FA_HEAD_DIM / 8), c8 = i % (FA_HEAD_DIM / 8), t = q0 + r / FA_GQA;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (t < S) v = *reinterpret_cast<const uint4*>(q + (size_t)t * FA_Q_SIZE + (kvh * FA_GQA + r % FA_GQA) * FA_HEAD_DIM + c8 * 8);
+        *reinterpret_cast<uint4*>(Qs + r * ATT_MMA_LD + c8 * 8) = v;
+    }
+    const int t_last = min(q0 + ATT_MMA_Q, S) - 1;
+    const int nchunks = t_last / ATT_MMA_KEYS + 1;
+    const int r0 = warp * 16 + g, r1 = r0 + 8;                     // this thread's two rows
+    const int t0 = q0 + r0 / FA_GQA, t1 = q0 + r1 / FA_GQA;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float o[FA_HEAD_DIM / 8][4];
+#pragma unroll
+    for (int nt = 0; nt < FA_HEAD_DIM / 8; ++nt) { o[nt][0] = 0.f; o[nt][1] = 0.f; o[nt][2] = 0.f; o[nt][3] = 0.f; }
+
+    for (int pass = 0; pass < 2; ++pass) {
+        for (int ch = 0; ch < nchunks; ++ch) {
+            const int j0 = ch * ATT_MMA_KEYS;
+            __syncthreads();
+            for (int i = tid; i < ATT_MMA_KEYS * (FA_HEAD_DIM / 8); i += 256) {
+                const int kk = i / (FA_HEAD_DIM / 8), c8 = i % (FA_HEAD_DIM / 8);
+                uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+                if (j0 + kk < S) {
+                    kv = *reinterpret_cast<const uint4*>(kb + (size_t)(j0 + kk) * FA_HEAD_DIM + c8 * 8);
+                    if (pass) vv = *reinterpret_cast<const uint4*>(vb + (size_t)(j0 + kk) * FA_HEAD_DIM + c8 * 8);
+                }
+                *reinterpret_cast<uint4*>(Ks + kk * ATT_MMA_LD + c8 * 8) = kv;
+                if (pass) *reinterpret_cast<uint4*>(Vs + kk * ATT_MMA_LD + c8 * 8) = vv;
+            }
+            __syncthreads();
+            // scores of this warp's 16 rows against the 64 keys
+            float sacc[ATT_MMA_KEYS / 8][4];
+#pragma unroll
+            for (int nt = 0; nt < ATT_MMA_KEYS / 8; ++nt) { sacc[nt][0] = 0.f; sacc[nt][1] = 0.f; sacc[nt][2] = 0.f; sacc[nt][3] = 0.f; }
+#pragma unroll 4
+            for (int ks = 0; ks < FA_HEAD_DIM / 16; ++ks) {
+                uint32_t a[4];
+                ldsm_x4(a, Qs + (warp * 16 + (lane & 15)) * ATT_MMA_LD + ks * 16 + (lane >> 4) * 8);
+#pragma unroll
+                for (int np = 0; np < ATT_MMA_KEYS / 16; ++np) {
+                    uint32_t b[4];
+                    ldsm_x4(b, Ks + (np * 16 + (lane & 7) + 8 * (lane >> 4)) * ATT_MMA_LD + ks * 16 + 8 * ((lane >> 3) & 1));
+                    mma_16816(sacc[2 * np], a, b[0], b[1]);
+                    mma_16816(sacc[2 * np + 1], a, b[2], b[3]);
+                }
+            }
+            // bf16 rounding, scale, causal mask
+#pragma unroll
+            for (int nt = 0; nt < ATT_MMA_KEYS / 8; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int j = j0 + nt * 8 + 2 * c + (e & 1);
+                    const int tr = (e < 2) ? t0 : t1;
+                    sacc[nt][e] = (j <= tr && tr < S) ? rbf(sacc[nt][e]) * 0.0625f : -INFINITY;
+                }
+            if (pass == 0) {
+                float cm0 = -INFINITY, cm1 = -INFINITY;
+#pragma unroll
+                for (int nt = 0; nt < ATT_MMA_KEYS / 8; ++nt) {
+                    cm0 = fmaxf(cm0, fmaxf(sacc[nt][0], sacc[nt][1]));
+                    cm1 = fmaxf(cm1, fmaxf(sacc[nt][2], sacc[nt][3]));
+                }
+                cm0 = fmaxf(cm0, __shfl_xor_sync(0xffffffffu, cm0, 1)); cm0 = fmaxf(cm0, __shfl_xor_sync(0xffffffffu, cm0, 2));
+                cm1 = fmaxf(cm1, __shfl_xor_sync(0xffffffffu, cm1, 1)); cm1 = fmaxf(cm1, __shfl_xor_sync(0xffffffffu, cm1, 2));
+                const float n0 = fmaxf(m0, cm0), n1 = fmaxf(m1, cm1);
+                float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+                for (int nt = 0; nt < ATT_MMA_KEYS / 8; ++nt) {
+                    if (n0 != -INFINITY) s0 += expf(sacc[nt][0] - n0) + expf(sacc[nt][1] - n0);
+                    if (n1 != -INFINITY) s1 += expf(sacc[nt][2] - n1) + expf(sacc[nt][3] - n1);
+                }
+                s0 += __shfl_xor_sync(0xffffffffu, s0, 1); s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+                s1 += __shfl_xor_sync(0xffffffffu, s1, 1); s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+                l0 = (m0 == -INFINITY ? 0.f : l0 * expf(m0 - n0)) + s0;
+                l1 = (m1 == -INFINITY ? 0.f : l1 * expf(m1 - n1)) + s1;
+                m0 = n0; m1 = n1;
+            } else {
+                // P in A-operand layout, then P.V
+#pragma unroll
+                for (int ks = 0; ks < ATT_MMA_KEYS / 16; ++ks) {
+                    uint32_t a[4];
+#pragma unroll
+                    for (int hf = 0; hf < 2; ++hf) {
+                        const float* sv = sacc[2 * ks + hf];
+                        const float p00 = (sv[0] == -INFINITY) ? 0.f : expf(sv[0] - m0) / l0, p01 = (sv[1] == -INFINITY) ? 0.f : expf(sv[1] - m0) / l0;
+                        const float p10 = (sv[2] == -INFINITY) ? 0.f : expf(sv[2] - m1) / l1, p11 = (sv[3] == -INFINITY) ? 0.f : expf(sv[3] - m1) / l1;
+                        const __nv_bfloat162 x0 = __floats2bfloat162_rn(p00, p01), x1 = __floats2bfloat162_rn(p10, p11);
+                        a[2 * hf] = *reinterpret_cast<const uint32_t*>(&x0);
+                        a[2 * hf + 1] = *reinterpret_cast<const uint32_t*>(&x1);
+                    }
+#pragma unroll
+                    for (int np = 0; np < FA_HEAD_DIM / 16; ++np) {
+                        uint32_t b[4];
+                        ldsm_x4_trans(b, Vs + (ks * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * ATT_MMA_LD + np * 16 + 8 * (lane >> 4));
+                        mma_16816(o[2 * np], a, b[0], b[1]);
+                        mma_16816(o[2 * np + 1], a, b[2], b[3]);
+                    }
+                }
+            }
+        }
+    }
+    // output: bf16(P.V) * bf16(sigmoid(gate)), rows r0 (o[.][0..1]) and r1 (o[.][2..3])
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+        const int r = hf ? r1 : r0, t = hf ? t1 : t0;
+        if (t >= S) continue;
+        const int head = kvh * FA_GQA + r % FA_GQA;
+        const bf16* gate = proj + (size_t)t * ldp + head * 2 * FA_HEAD_DIM + FA_HEAD_DIM;
+        bf16* dst = out + (size_t)t * FA_Q_SIZE + head * FA_HEAD_DIM;
+#pragma unroll
+        for (int nt = 0; nt < FA_HEAD_DIM / 8; ++nt) {
+            const int d = nt * 8 + 2 * c;
+            const uint32_t gr = *reinterpret_cast<const uint32_t*>(gate + d);
+            const __nv_bfloat162 pr = __halves2bfloat162(f2bf(rbf(o[nt][2 * hf]) * rbf(sigmoid_f(bf_lo(gr)))), f2bf(rbf(o[nt][2 * hf + 1]) * rbf(sigmoid_f(bf_hi(gr)))));
+            *reinterpret_cast<__nv_bfloat162*>(dst + d) = pr;
+        }
+    }
+}
+
 // ---- last-token LM head: GEMV over the vocabulary + arg-max (lowest index among equal bf16 maxima) -----
 static __global__ void __launch_bounds__(256) pf_lm_head_kernel(const bf16* __restrict__ x, const bf16* __restrict__ lm, float* __restrict__ bmv,
                                                          int* __restrict__ bmi, float* __restrict__ logits_out) {
