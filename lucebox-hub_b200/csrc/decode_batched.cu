@@ -159,45 +159,86 @@ __device__ __forceinline__ const bf16* kv_row_c(const bf16* pages, const int* tb
     return pages + (((size_t)tb[pos / KV_PAGE] * FA_KV_HEADS + kvh) * KV_PAGE + (pos % KV_PAGE)) * FA_HEAD_DIM;
 }
 
+// Both kernels stage the chunk's K (or V) rows in shared memory (rows padded to 528 bytes) with coalesced 16-byte
+// reads through the page table and run mma.sync m16n8k16 tiles on them: the M side holds the four q heads of the kv
+// head (rows 4-15 of the tile are zero), so a position costs a handful of instructions instead of a warp reduction
+// per head.  Fragment loads are ldmatrix (ldsm_x4 / ldsm_x4_trans of the prefill attention).
+constexpr int BD_LD = FA_HEAD_DIM + 8;                   // shared-memory row, bf16 elements
+constexpr int BD_PLD = BD_CHUNK + 8;
+constexpr int BD_SC_SMEM = (16 + BD_CHUNK) * BD_LD * 2;
+constexpr int BD_PV_SMEM = (BD_CHUNK * BD_LD + 16 * BD_PLD) * 2;
+
+// stage the chunk's rows [j0, j0+cn) of one kv head into shared memory with cp.async (a warp copies one 512-byte row
+// per step, every copy of the chunk in flight at once); the chunk is two 64-position pages (j0 is a multiple of 128)
+__device__ __forceinline__ void bd_stage_rows(const bf16* __restrict__ pages, const int* __restrict__ tb, int kvh, int j0, int cn, bf16* dst_rows) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bf16* pg[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+        pg[h] = (h * KV_PAGE < cn) ? pages + (((size_t)tb[j0 / KV_PAGE + h] * FA_KV_HEADS + kvh) * KV_PAGE) * FA_HEAD_DIM : pages;
+#pragma unroll 8
+    for (int it = 0; it < BD_CHUNK / 4; ++it) {              // all 32 copies of a thread are in flight together
+        const int kk = it * 4 + warp;
+        bf16* d = dst_rows + kk * BD_LD + lane * 8;
+        if (kk < cn) {
+            const uint32_t da = (uint32_t)__cvta_generic_to_shared(d);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(da), "l"(pg[kk / KV_PAGE] + (size_t)(kk % KV_PAGE) * FA_HEAD_DIM + lane * 8) : "memory");
+        } else {
+            *reinterpret_cast<uint4*>(d) = make_uint4(0, 0, 0, 0);
+        }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
 __global__ void __launch_bounds__(128) bd_att_scores_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k_pages,
                                                             const int* __restrict__ positions, const int* __restrict__ table, int max_pages,
                                                             float* __restrict__ scores, float* __restrict__ stats, int max_ctx, int max_chunks) {
+    extern __shared__ __align__(16) unsigned char bd_sm[];
     __shared__ float ssc[FA_GQA][BD_CHUNK];
-    const int b = blockIdx.x, kvh = blockIdx.y, c = blockIdx.z, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    bf16* Qs = reinterpret_cast<bf16*>(bd_sm);           // [16][BD_LD], rows 0-3 = the q heads of this kv head
+    bf16* Ks = Qs + 16 * BD_LD;                          // [BD_CHUNK][BD_LD]
+    const int b = blockIdx.x, kvh = blockIdx.y, c = blockIdx.z, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int L = positions[b] + 1, j0 = c * BD_CHUNK;
     if (j0 >= L) return;
-    const int j1 = min(L, j0 + BD_CHUNK);
+    const int j1 = min(L, j0 + BD_CHUNK), cn = j1 - j0;
     const int* tb = table + b * max_pages;
-    float qr[FA_GQA][8];
-#pragma unroll
-    for (int g = 0; g < FA_GQA; ++g) {
-        const uint4 qv = *(reinterpret_cast<const uint4*>(q + (size_t)b * FA_Q_SIZE + (kvh * FA_GQA + g) * FA_HEAD_DIM) + lane);
-        qr[g][0] = bf_lo(qv.x); qr[g][1] = bf_hi(qv.x); qr[g][2] = bf_lo(qv.y); qr[g][3] = bf_hi(qv.y);
-        qr[g][4] = bf_lo(qv.z); qr[g][5] = bf_hi(qv.z); qr[g][6] = bf_lo(qv.w); qr[g][7] = bf_hi(qv.w);
+    for (int i = tid; i < 16 * (FA_HEAD_DIM / 8); i += 128) {
+        const int r = i / (FA_HEAD_DIM / 8), c8 = i % (FA_HEAD_DIM / 8);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r < FA_GQA) v = *reinterpret_cast<const uint4*>(q + (size_t)b * FA_Q_SIZE + (kvh * FA_GQA + r) * FA_HEAD_DIM + c8 * 8);
+        *reinterpret_cast<uint4*>(Qs + r * BD_LD + c8 * 8) = v;
     }
-    for (int j = j0 + warp; j < j1; j += 8) {          // two positions in flight per warp
-        const int jb = j + 4;
-        const uint4 ka = *(reinterpret_cast<const uint4*>(kv_row_c(k_pages, tb, kvh, j)) + lane);
-        const uint4 kb = (jb < j1) ? *(reinterpret_cast<const uint4*>(kv_row_c(k_pages, tb, kvh, jb)) + lane) : make_uint4(0, 0, 0, 0);
+    bd_stage_rows(k_pages, tb, kvh, j0, cn, Ks);
+    __syncthreads();
+    // warp w: keys [32w, 32w+32) = 4 tiles of 8 keys
+    float acc[4][4];
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-            const int jj = r ? jb : j;
-            if (jj >= j1) break;
-            const uint4 kv = r ? kb : ka;
-            const float kf[8] = {bf_lo(kv.x), bf_hi(kv.x), bf_lo(kv.y), bf_hi(kv.y), bf_lo(kv.z), bf_hi(kv.z), bf_lo(kv.w), bf_hi(kv.w)};
+    for (int nt = 0; nt < 4; ++nt) { acc[nt][0] = 0.f; acc[nt][1] = 0.f; acc[nt][2] = 0.f; acc[nt][3] = 0.f; }
+#pragma unroll 4
+    for (int ks = 0; ks < FA_HEAD_DIM / 16; ++ks) {
+        uint32_t a[4];
+        ldsm_x4(a, Qs + (lane & 15) * BD_LD + ks * 16 + (lane >> 4) * 8);
 #pragma unroll
-            for (int g = 0; g < FA_GQA; ++g) {
-                float d = 0.f;
+        for (int np = 0; np < 2; ++np) {
+            uint32_t bb[4];
+            ldsm_x4(bb, Ks + (warp * 32 + np * 16 + (lane & 7) + 8 * (lane >> 4)) * BD_LD + ks * 16 + 8 * ((lane >> 3) & 1));
+            mma_16816(acc[2 * np], a, bb[0], bb[1]);
+            mma_16816(acc[2 * np + 1], a, bb[2], bb[3]);
+        }
+    }
+    {   // accumulator rows 0-3 (g = lane/4 < 4) are the four heads; columns 2c, 2c+1 of each 8-key tile
+        const int g = lane >> 2, cc = lane & 3;
+        if (g < FA_GQA) {
 #pragma unroll
-                for (int i = 0; i < 8; ++i) d = fmaf(qr[g][i], kf[i], d);
-                d = warp_sum(d);
-                if (lane == 0) ssc[g][jj - j0] = rbf(d) * 0.0625f;
+            for (int nt = 0; nt < 4; ++nt) {
+                ssc[g][warp * 32 + nt * 8 + 2 * cc] = rbf(acc[nt][0]) * 0.0625f;
+                ssc[g][warp * 32 + nt * 8 + 2 * cc + 1] = rbf(acc[nt][1]) * 0.0625f;
             }
         }
     }
     __syncthreads();
-    const int cn = j1 - j0;
-    {   // warp g: statistics of head g over this chunk; all threads: scores to global
+    {   // warp g: statistics of head g over this chunk; scores to global
         const int g = warp;
         float mx = -INFINITY;
         for (int j = lane; j < cn; j += 32) mx = fmaxf(mx, ssc[g][j]);
@@ -218,8 +259,10 @@ __global__ void __launch_bounds__(128) bd_att_scores_kernel(const bf16* __restri
 __global__ void __launch_bounds__(128) bd_att_pv_kernel(const bf16* __restrict__ v_pages, const int* __restrict__ positions,
                                                         const int* __restrict__ table, int max_pages, const float* __restrict__ scores,
                                                         const float* __restrict__ stats, float* __restrict__ partial, int max_ctx, int max_chunks) {
-    __shared__ float sp[FA_GQA][BD_CHUNK];
+    extern __shared__ __align__(16) unsigned char bd_sm[];
     __shared__ float sml[FA_GQA][2];
+    bf16* Vs = reinterpret_cast<bf16*>(bd_sm);           // [BD_CHUNK][BD_LD]
+    bf16* Ps = Vs + BD_CHUNK * BD_LD;                    // [16][BD_PLD], rows 0-3 = P of the four heads
     const int b = blockIdx.x, kvh = blockIdx.y, c = blockIdx.z, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int L = positions[b] + 1, j0 = c * BD_CHUNK;
     if (j0 >= L) return;
@@ -237,31 +280,37 @@ __global__ void __launch_bounds__(128) bd_att_pv_kernel(const bf16* __restrict__
         sm = warp_sum(sm);
         if (lane == 0) { sml[warp][0] = mx; sml[warp][1] = sm; }
     }
+    bd_stage_rows(v_pages, tb, kvh, j0, cn, Vs);
     __syncthreads();
-    for (int i = tid; i < FA_GQA * cn; i += 128) {
-        const int g = i / cn, j = i % cn;
-        sp[g][j] = rbf(expf(scores[((size_t)b * FA_Q_HEADS + kvh * FA_GQA + g) * max_ctx + j0 + j] - sml[g][0]) / sml[g][1]);
+    for (int i = tid; i < 16 * BD_CHUNK; i += 128) {
+        const int g = i / BD_CHUNK, j = i % BD_CHUNK;
+        float pv = 0.f;
+        if (g < FA_GQA && j < cn) pv = rbf(expf(scores[((size_t)b * FA_Q_HEADS + kvh * FA_GQA + g) * max_ctx + j0 + j] - sml[g][0]) / sml[g][1]);
+        Ps[g * BD_PLD + j] = f2bf(pv);
     }
     __syncthreads();
-    float acc[FA_GQA][2];
+    // warp w: output dims [64w, 64w+64) = 8 tiles of 8 dims; 8 steps of 16 keys
+    float acc[8][4];
 #pragma unroll
-    for (int g = 0; g < FA_GQA; ++g) { acc[g][0] = 0.f; acc[g][1] = 0.f; }
-    for (int j = 0; j < cn; j += 4) {
-        uint32_t vr[4];
+    for (int nt = 0; nt < 8; ++nt) { acc[nt][0] = 0.f; acc[nt][1] = 0.f; acc[nt][2] = 0.f; acc[nt][3] = 0.f; }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) vr[u] = (j + u < cn) ? *(reinterpret_cast<const uint32_t*>(kv_row_c(v_pages, tb, kvh, j0 + j + u)) + tid) : 0u;
+    for (int ks = 0; ks < BD_CHUNK / 16; ++ks) {
+        uint32_t a[4];
+        ldsm_x4(a, Ps + (lane & 15) * BD_PLD + ks * 16 + (lane >> 4) * 8);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            if (j + u < cn) {
-                const float v0 = bf_lo(vr[u]), v1 = bf_hi(vr[u]);
-#pragma unroll
-                for (int g = 0; g < FA_GQA; ++g) { const float p = sp[g][j + u]; acc[g][0] = fmaf(p, v0, acc[g][0]); acc[g][1] = fmaf(p, v1, acc[g][1]); }
-            }
+        for (int np = 0; np < 4; ++np) {
+            uint32_t bb[4];
+            ldsm_x4_trans(bb, Vs + (ks * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * BD_LD + warp * 64 + np * 16 + 8 * (lane >> 4));
+            mma_16816(acc[2 * np], a, bb[0], bb[1]);
+            mma_16816(acc[2 * np + 1], a, bb[2], bb[3]);
         }
     }
+    const int g = lane >> 2, cc = lane & 3;
+    if (g < FA_GQA) {
+        float* dst = partial + (((size_t)b * FA_Q_HEADS + kvh * FA_GQA + g) * max_chunks + c) * FA_HEAD_DIM + warp * 64 + 2 * cc;
 #pragma unroll
-    for (int g = 0; g < FA_GQA; ++g)
-        reinterpret_cast<float2*>(partial + (((size_t)b * FA_Q_HEADS + kvh * FA_GQA + g) * max_chunks + c) * FA_HEAD_DIM)[tid] = make_float2(acc[g][0], acc[g][1]);
+        for (int nt = 0; nt < 8; ++nt) *reinterpret_cast<float2*>(dst + nt * 8) = make_float2(acc[nt][0], acc[nt][1]);
+    }
 }
 
 __global__ void __launch_bounds__(256) bd_att_merge_kernel(const float* __restrict__ partial, const int* __restrict__ positions,
@@ -378,6 +427,12 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
         fused_h = reinterpret_cast<const PrefillFusedB*>(f);
         if (!layers_h) return QWEN35_ERR_CUDA;
     }
+    static bool attr_done = false;
+    if (!attr_done) {
+        Q35_CUDA_OK(cudaFuncSetAttribute(bd_att_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BD_SC_SMEM));
+        Q35_CUDA_OK(cudaFuncSetAttribute(bd_att_pv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BD_PV_SMEM));
+        attr_done = true;
+    }
     // scratch rows of B tokens
     const size_t rows = (size_t)B;
     const size_t n_hidden = rows * HIDDEN, n_proj = rows * DN_PROJ_ROWS, n_att = rows * 2048, n_mlp = rows * INTER, n_logits = rows * VOCAB;
@@ -434,8 +489,8 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
             bd_qk_norm_rope_kernel<<<(B * 12 + 7) / 8, 256, 0, stream>>>(proj, ldp, (const bf16*)L.p[FA_QNORM], (const bf16*)L.p[FA_KNORM], rt,
                                                                          in->positions, in->block_table, in->max_pages, qbuf, kp, vp, B);
             const dim3 agrid(B, FA_KV_HEADS, max_chunks);
-            bd_att_scores_kernel<<<agrid, 128, 0, stream>>>(qbuf, kp, in->positions, in->block_table, in->max_pages, att_scores, att_stats, in->max_ctx, max_chunks);
-            bd_att_pv_kernel<<<agrid, 128, 0, stream>>>(vp, in->positions, in->block_table, in->max_pages, att_scores, att_stats, att_part, in->max_ctx, max_chunks);
+            bd_att_scores_kernel<<<agrid, 128, BD_SC_SMEM, stream>>>(qbuf, kp, in->positions, in->block_table, in->max_pages, att_scores, att_stats, in->max_ctx, max_chunks);
+            bd_att_pv_kernel<<<agrid, 128, BD_PV_SMEM, stream>>>(vp, in->positions, in->block_table, in->max_pages, att_scores, att_stats, att_part, in->max_ctx, max_chunks);
             bd_att_merge_kernel<<<(B * FA_Q_HEADS + 7) / 8, 256, 0, stream>>>(att_part, in->positions, proj, ldp, attn, B, max_chunks);
             g_launches.fetch_add(4);
             w_out = (const bf16*)L.p[FA_O]; w_post = (const bf16*)L.p[FA_POST_NORM]; w_down = (const bf16*)L.p[FA_DOWN];
