@@ -190,7 +190,7 @@ def tree_verify_bench(dev, n_nodes=33, ctx=4096, iters=5):
             "roofline_frac": alg / (ms * 1e-3) / 1e9 / measured_peak()[0], "tflops": flops / (ms * 1e-3) / 1e12}
 
 
-def batched_decode_bench(weights_gpu, dev, rank, n_seq, ctx, n_steps):
+def batched_decode_bench(weights_gpu, dev, rank, n_seq, ctx, n_steps, kernel_table=False):
     """`n_seq` independent sequences per GPU, `ctx`-token contexts prefilled by the library's own
     prefill, `n_steps` greedy steps.  Returns (tok/s on this rank, ms per step, algorithmic bytes per step)."""
     from qwen35_b200.config import QWEN35_0P8B as D
@@ -212,6 +212,13 @@ def batched_decode_bench(weights_gpu, dev, rank, n_seq, ctx, n_steps):
     e1.record()
     torch.cuda.synchronize(dev)
     bd.check_status()
+    if kernel_table:
+        # device time per kernel of ONE step (torch.profiler / CUPTI), printed to stderr for profiles/
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            bd.step(graph=True)
+            torch.cuda.synchronize(dev)
+        print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=20, max_name_column_width=60), file=sys.stderr)
     ms = e0.elapsed_time(e1)
     mid = ctx + n_steps // 2
     bytes_step = 2 * (498_113_344 + 254_279_680) + n_seq * (2 * 18 * 16 * 128 * 128 * 4 + 2 * 18 * 6144 * 4 * 4 + 12288 * (mid + 2))
@@ -387,7 +394,7 @@ def run_ours(args):
         tree = tree_verify_bench(dev)
     batched = None
     if args.batched > 0:
-        b_tok_s, b_ms, b_bytes = batched_decode_bench(wg, dev, rank, args.batched, args.batched_ctx, GEN)
+        b_tok_s, b_ms, b_bytes = batched_decode_bench(wg, dev, rank, args.batched, args.batched_ctx, GEN, kernel_table=args.kernel_table and rank == 0)
         bt = torch.tensor([b_tok_s, b_ms], dtype=torch.float64, device=dev)
         if world > 1:
             import torch.distributed as dist
@@ -463,6 +470,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batched", type=int, default=64, help="sequences per GPU for the batched-decode section (0 = skip)")
     ap.add_argument("--batched-ctx", type=int, default=2048)
+    ap.add_argument("--kernel-table", action="store_true", help="print the per-kernel device times of one batched step to stderr")
     ap.add_argument("--prefill-sweep", default="128,512,1024,4096", help="prompt lengths of the prefill sweep ('' = skip)")
     ap.add_argument("--tree-verify", type=int, default=1, help="run the 27B-class tree-verify section (0 = skip)")
     ap.add_argument("--prompt", type=int, default=520, help="prompt tokens (smaller values are for profiler captures)")
