@@ -260,6 +260,28 @@ def cpu_baseline(weights_cpu, ids, n_decode=16, use_hf=False):
             "pp520_tok_s": PROMPT / t_pp}
 
 
+def tree_cpu_baseline(n_nodes=8, layers=2, vocab=4096):
+    """CPU side of BASELINE configs[4]: the path-sequential oracle at the 27B widths on a reduced model (`layers` of
+    64 layers, one DeltaNet + one attention; `vocab` of 248 320 LM-head rows; an 8-node chain on an empty context),
+    timed per node-layer and extrapolated to 33 nodes x 64 layers.  Reported, not a target."""
+    import dataclasses
+    from oracle.tree_verify_oracle import TreeOracle
+    from qwen35_b200.tree_verify import QWEN35_27B, make_random_tree_weights
+    cores = host_cores()
+    torch.set_num_threads(cores)
+    T = dataclasses.replace(QWEN35_27B, n_layers=layers, fa_period=2, vocab=vocab)
+    w = make_random_tree_weights(T, 11)
+    orc = TreeOracle(T, w, 64)
+    tokens = list(range(1, n_nodes + 1))
+    t0 = time.perf_counter()
+    orc.verify(tokens, [-1] + list(range(n_nodes - 1)))
+    dt = time.perf_counter() - t0
+    per_node_layer = dt / (n_nodes * layers)
+    return {"value": per_node_layer * 33 * 64 * 1e3, "unit": "ms per verify (extrapolated)", "cores": cores, "kind": "port",
+            "sample": f"{n_nodes}-node chain through {layers} of 64 layers at 27B widths (vocab {vocab}), {dt:.1f} s measured, "
+                      f"scaled by 33*64/({n_nodes}*{layers}); weights dequantised once beforehand"}
+
+
 def run_reference(args):
     rank, _, world = dist_env()
     if rank != 0:
@@ -456,6 +478,11 @@ def run_ours(args):
             line["tree_verify"] = tree
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(w_cpu, ids_cpu, 16, use_hf=False)
+            if batched:
+                # the CPU runs the sequences one after another, so its aggregate rate is its single-sequence rate
+                batched["cpu_baseline"] = dict(line["cpu_baseline"], sample="single-sequence decode rate of the bs=1 sample (the CPU path has no batching); context 520 instead of 2048")
+            if tree:
+                tree["cpu_baseline"] = tree_cpu_baseline()
         print(json.dumps(line))
     if world > 1:
         torch.distributed.destroy_process_group()
