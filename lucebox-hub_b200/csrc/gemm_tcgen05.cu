@@ -350,7 +350,11 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
 // The activation box holds 64 rows; the MMA reads 128, so accumulator rows 64-127 are garbage and are never read.
 // ncu on the gate/up shape (33 x 17408 x 5120): tensor pipe 10 % active, issue slots 61 % busy, 10 instructions per
 // weight: the kernel is bound by the dequantisation arithmetic, not by HBM (13 %) or the MMA.
-// value = bf16((d*sc)*q - dmin*m) with separate f32 roundings, the published Q4_K dequantisation.
+// The weight operand is value = fma_bf16(q, bf16(d*sc), -bf16(dmin*m)), two weights per instruction: the published f32
+// dequantisation (d*sc)*q - dmin*m followed by a rounding to bf16 costs ~10 instructions per weight on the CUDA cores
+// and bounded the kernel.  qwen35_b200_dequant_q4k keeps the published arithmetic bit for bit.  (An f16 weight
+// operand beside bf16 activations is not an option: kind::f16 with different A and B formats raised "illegal
+// instruction" on this GPU.)
 constexpr int Q4K_THREADS = 576;                                                      // 2 + 16 dequantisation warps
 constexpr int Q4K_DQ_WARPS = 16;
 constexpr int Q4K_STAGES = 3, Q4K_RAW_STAGES = 3;
@@ -488,29 +492,30 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
             float sc0, m0, sc1, m1;
             q4k_scale_min_u32(hd.y, hd.z, hd.w, 2 * g, sc0, m0);
             q4k_scale_min_u32(hd.y, hd.z, hd.w, 2 * g + 1, sc1, m1);
-            const float d0 = __fmul_rn(d, sc0), mm0 = __fmul_rn(dmin, m0), d1 = __fmul_rn(d, sc1), mm1 = __fmul_rn(dmin, m1);
+            // operand value = bf16 fma(q, bf16(d*sc), -bf16(dmin*m)): d*sc and dmin*m are exact in f32 (11 + 6 bits), one
+            // rounding each to bf16, then one fused rounding; two weights per instruction
+            const __nv_bfloat162 ds0 = __float2bfloat162_rn(__fmul_rn(d, sc0)), ds1 = __float2bfloat162_rn(__fmul_rn(d, sc1));
+            const __nv_bfloat162 nm0 = __hneg2(__float2bfloat162_rn(__fmul_rn(dmin, m0))), nm1 = __hneg2(__float2bfloat162_rn(__fmul_rn(dmin, m1)));
+            const __nv_bfloat162 k128 = __float2bfloat162_rn(128.0f);
             const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
             unsigned char* brow = tiles_ptr + st * Q4K_STAGE_BYTES + 2 * Q4K_A_SLAB + h * Q4K_B_SLAB + row * 128;
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) {                    // cc 0,1: low nibbles; 2,3: high nibbles
                 const bool hi = cc >= 2;
                 const int c = (hi ? 4 : 0) + 2 * part + (cc & 1);     // chunk = weights 8c..8c+7 of the group
-                const float dx = hi ? d1 : d0, mx = hi ? mm1 : mm0;
+                const __nv_bfloat162 dsx = hi ? ds1 : ds0, nmx = hi ? nm1 : nm0;
                 uint32_t o[4];
 #pragma unroll
                 for (int h2 = 0; h2 < 2; ++h2) {
                     const uint32_t word = w[2 * (cc & 1) + h2];
                     const uint32_t nib = (hi ? (word >> 4) : word) & 0x0F0F0F0Fu;
-                    // nibble -> float without the slow integer conversion: 0x4B0000qq is 2^23 + q exactly
-                    const float f0 = __fsub_rn(__uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7650)), 8388608.0f);
-                    const float f1 = __fsub_rn(__uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7651)), 8388608.0f);
-                    const float f2 = __fsub_rn(__uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7652)), 8388608.0f);
-                    const float f3 = __fsub_rn(__uint_as_float(__byte_perm(nib, 0x4B000000u, 0x7653)), 8388608.0f);
-                    const float v0 = __fsub_rn(__fmul_rn(dx, f0), mx), v1 = __fsub_rn(__fmul_rn(dx, f1), mx);
-                    const float v2 = __fsub_rn(__fmul_rn(dx, f2), mx), v3 = __fsub_rn(__fmul_rn(dx, f3), mx);
-                    const __nv_bfloat162 p0 = __floats2bfloat162_rn(v0, v1), p1 = __floats2bfloat162_rn(v2, v3);
-                    o[2 * h2] = *reinterpret_cast<const uint32_t*>(&p0);
-                    o[2 * h2 + 1] = *reinterpret_cast<const uint32_t*>(&p1);
+                    // bytes (q, 0x43) are the bf16 numbers 128 + q: exact, no integer conversion
+                    const uint32_t u01 = __byte_perm(nib, 0x43004300u, 0x7150), u23 = __byte_perm(nib, 0x43004300u, 0x7352);
+                    const __nv_bfloat162 x01 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&u01), k128);
+                    const __nv_bfloat162 x23 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&u23), k128);
+                    const __nv_bfloat162 y01 = __hfma2(x01, dsx, nmx), y23 = __hfma2(x23, dsx, nmx);
+                    o[2 * h2] = *reinterpret_cast<const uint32_t*>(&y01);
+                    o[2 * h2 + 1] = *reinterpret_cast<const uint32_t*>(&y23);
                 }
                 *reinterpret_cast<uint4*>(brow + ((c ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
             }

@@ -11,7 +11,8 @@ models/qwen35_27b/src/qwen35_target_graph.cpp:281-804 and the tree semantics of 
 path-recursively (no mask, no DFS tricks) so it checks the mask / parent-chain logic of the product independently.
 
 Rounding points (shared with the product by definition, since nothing upstream pins them): activations between
-operators are bf16; a Q4_K linear uses bf16(dequantised weight) with f32 accumulation and returns bf16; norms, RoPE,
+operators are bf16; a Q4_K linear uses the bf16 weight operand of `q4k_gemm_operand` (embedding rows: bf16 of the
+published dequantisation) with f32 accumulation and returns bf16; norms, RoPE,
 softmax, conv, the delta rule and its state are f32; attention probabilities are rounded to bf16 before P.V; a node's
 DeltaNet post-state is kept as f16 and a node that is not its parent's first child (DFS index parent+1) starts from
 that f16 copy (qwen35_target_graph.cpp:540-583: the kernel reloads state at DFS branch transitions)."""
@@ -46,6 +47,45 @@ def q4k_dequant(blocks: np.ndarray) -> np.ndarray:
     return out
 
 
+def _f64_to_bf16_once(x: np.ndarray) -> np.ndarray:
+    """f64 -> bf16 with ONE round-to-nearest-even (returned as f32): first to f32 with round-to-odd (truncate toward
+    zero, set the last bit if anything was lost), which makes the second rounding to 8 bits safe."""
+    y = x.astype(np.float32)
+    over = np.abs(y.astype(np.float64)) > np.abs(x)
+    y = np.where(over, np.nextafter(y, np.float32(0)), y).astype(np.float32)
+    inexact = y.astype(np.float64) != x
+    bits = y.view(np.uint32)
+    y = np.where(inexact, bits | np.uint32(1), bits).astype(np.uint32).view(np.float32)
+    return torch.from_numpy(y.copy()).bfloat16().float().numpy()
+
+
+def q4k_gemm_operand(blocks: np.ndarray) -> np.ndarray:
+    """[n, 144] uint8 -> [n, 256] f32 holding the bf16 weight operand of the product's Q4_K GEMM:
+    fma_bf16(q, bf16(d*sc), -bf16(dmin*m)) -- d*sc and dmin*m are exact in f32, rounded once to bf16; the fused
+    multiply-add is evaluated exactly in f64 and rounded once to bf16."""
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1, 144)
+    n = blocks.shape[0]
+    d = blocks[:, 0:2].copy().view(np.float16).astype(np.float32).reshape(n)
+    dmin = blocks[:, 2:4].copy().view(np.float16).astype(np.float32).reshape(n)
+    s = blocks[:, 4:16].astype(np.int32)
+    qs = blocks[:, 16:144]
+    out = np.zeros((n, 256), np.float32)
+    tobf = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).bfloat16().float().numpy().astype(np.float64)   # noqa: E731
+    for j in range(8):
+        if j < 4:
+            sc = s[:, j] & 63; mn = s[:, j + 4] & 63
+        else:
+            sc = (s[:, j + 4] & 0xF) | ((s[:, j - 4] >> 6) << 4)
+            mn = (s[:, j + 4] >> 4) | ((s[:, j] >> 6) << 4)
+        dsc = tobf(d * sc.astype(np.float32))[:, None]
+        mm = tobf(dmin * mn.astype(np.float32))[:, None]
+        g, half = j // 2, j % 2
+        q = qs[:, 32 * g:32 * g + 32]
+        q = (q >> 4) if half else (q & 0xF)
+        out[:, 32 * j:32 * j + 32] = _f64_to_bf16_once(q.astype(np.float64) * dsc - mm)
+    return out
+
+
 def rb(x: torch.Tensor) -> torch.Tensor:
     return x.bfloat16().float()
 
@@ -58,7 +98,7 @@ class TreeOracle:
 
         def mat(blocks):
             r, nb, _ = blocks.shape
-            return rb(torch.from_numpy(q4k_dequant(blocks.numpy().reshape(-1, 144))).reshape(r, nb * 256))
+            return torch.from_numpy(q4k_gemm_operand(blocks.numpy().reshape(-1, 144))).reshape(r, nb * 256)
 
         self.layers = []
         for L in weights["layers"]:

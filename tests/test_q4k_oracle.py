@@ -3,7 +3,7 @@ import numpy as np
 import pytest
 import torch
 
-from oracle.tree_verify_oracle import TreeOracle, q4k_dequant
+from oracle.tree_verify_oracle import TreeOracle, q4k_dequant, q4k_gemm_operand
 
 
 def _blocks(n, seed):
@@ -57,3 +57,12 @@ def test_accept_walk():
     assert path == [0, 1, 2] and nxt == 4
     path, nxt = TreeOracle.accept(tokens, parents, [8, 9, 4, 3, 1])
     assert path == [0] and nxt == 8
+
+
+def test_q4k_gemm_operand_is_close_to_the_published_value():
+    """The bf16 operand of the GEMM differs from the published f32 dequantisation by bf16 roundings only."""
+    b = _blocks(64, 9)
+    ref, got = q4k_dequant(b), q4k_gemm_operand(b)
+    scale = np.abs(ref).max(axis=1, keepdims=True) + 1e-12
+    assert float((np.abs(got - ref) / scale).max()) < 2.0 ** -6
+    assert np.array_equal(got, torch.from_numpy(got).bfloat16().float().numpy())      # every value is a bf16 number

@@ -36,16 +36,16 @@ def test_q4k_dequant_gpu_bit_exact():
 @pytest.mark.parametrize("M,N,K,epi", [(33, 512, 512, 0), (7, 1000, 1024, 0), (40, 2048, 5120, 1), (33, 1024, 17408, 1), (33, 3584, 1024, 2),
                                        (1, 128, 256, 0), (64, 640, 768, 2)])
 def test_q4k_gemm_matches_dequantised_reference(M, N, K, epi):
-    """Fused dequantisation GEMM against torch on the dequantised (bf16-rounded) weights: same values, f32 sums in a
+    """Fused dequantisation GEMM against torch on the oracle's bf16 weight operand: same values, f32 sums in a
     different order, so a few outputs may land one bf16 step away."""
     import ctypes as C
-    from oracle.tree_verify_oracle import q4k_dequant
+    from oracle.tree_verify_oracle import q4k_gemm_operand
     from qwen35_b200 import _capi
     from qwen35_b200.tree_verify import random_q4k
     torch.manual_seed(M + N)
     rows = 2 * N if epi == 2 else N
     blocks = random_q4k(rows, K, 17 + N, sigma=0.05)
-    W = torch.from_numpy(q4k_dequant(blocks.numpy().reshape(-1, 144))).reshape(rows, K).bfloat16().float().cuda()
+    W = torch.from_numpy(q4k_gemm_operand(blocks.numpy().reshape(-1, 144))).reshape(rows, K).cuda()
     A = torch.randn(M, K, device="cuda").bfloat16()
     R = torch.randn(M, N, device="cuda").bfloat16()
     out = torch.zeros(M, N, dtype=torch.bfloat16, device="cuda")
