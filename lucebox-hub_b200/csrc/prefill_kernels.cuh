@@ -122,11 +122,14 @@ static __global__ void pf_conv_state_kernel(const bf16* __restrict__ proj, int l
 // ---- chunk-local part of the gated delta rule: one CTA (256 threads) per (chunk, head) --------------
 // Per chunk of 64 tokens (zero padded): gc = cumsum(g); T = (I + tril(-(k beta) k^T * decay, -1))^-1 by forward
 // substitution; vprime = T (v beta); kcd = T (k beta exp(gc)); aqk = tril(q k^T * decay).  All f32.
-struct ChunkScratch {          // one record per (head, chunk), floats
+struct ChunkScratch {          // one record per (head, chunk), floats; every array starts on a 16-byte boundary
     float vprime[DN_CHUNK][DN_V];
     float kcd[DN_CHUNK][DN_K];
+    float qs[DN_CHUNK][DN_K];      // q / sqrt(128) * exp(gc_i): the scan's left operand of q S
+    float ks[DN_CHUNK][DN_K];      // k * exp(gc_last - gc_i):   the scan's left operand of the state update
     float aqk[DN_CHUNK][DN_CHUNK];
     float gc[DN_CHUNK];
+    float eg_last[4];              // [0] = exp(gc_last)
 };
 
 constexpr int CHUNK_LOCAL_SMEM = (2 * DN_CHUNK * (DN_K + 1) + DN_CHUNK * DN_V + DN_CHUNK * (DN_CHUNK + 1) + 3 * DN_CHUNK) * 4;
@@ -171,6 +174,15 @@ static __global__ void __launch_bounds__(256) pf_dn_chunk_local_kernel(const bf1
     if (tid < DN_CHUNK) { se[tid] = expf(sg[tid]); out.gc[tid] = sg[tid]; }
     for (int e = tid; e < DN_CHUNK * DN_V; e += 256) sv[e >> 7][e & 127] *= sb[e >> 7];      // v * beta
     __syncthreads();
+    {   // operands of the scan that depend on this chunk only
+        const float g_last = sg[DN_CHUNK - 1];
+        for (int e = tid; e < DN_CHUNK * DN_K; e += 256) {
+            const int i = e >> 7, d = e & 127;
+            out.qs[i][d] = sq[i][d] * se[i];
+            out.ks[i][d] = sk[i][d] * expf(g_last - sg[i]);
+        }
+        if (tid == 0) out.eg_last[0] = expf(g_last);
+    }
     // A[i][j] = -(beta_i k_i . k_j) * exp(gc_i - gc_j) for j < i, else 0;   aqk[i][j] = (q_i . k_j) * exp(gc_i - gc_j) for j <= i
     for (int e = tid; e < DN_CHUNK * DN_CHUNK; e += 256) {
         const int i = e >> 6, j = e & 63;
@@ -211,101 +223,145 @@ static __global__ void __launch_bounds__(256) pf_dn_chunk_local_kernel(const bf1
     }
 }
 
-// ---- scan over chunks: one CTA (256 threads) per (head, 16-wide slice of the value dimension) --------
+// ---- scan over chunks: one CTA (512 threads) per (head, 16-wide slice of the value dimension) --------
+// Sequential over the chunks of a head; per chunk  v_new = vprime - kcd S,  out = qs S + aqk v_new,
+// S <- S exp(gc_last) + ks^T v_new  (S = state slice [128 k][16 v] in shared memory, all f32).  The operands are
+// plain copies of what the chunk-local kernel wrote, so they arrive by cp.async while the previous phase computes:
+// group 1 = {kcd, qs, vprime slice} (first phase), group 2 = {aqk, ks} (second and third), each refilled as soon
+// as its buffers are free.
 constexpr int SCAN_VW = 16;
-constexpr int CHUNK_SCAN_SMEM = (3 * DN_CHUNK * (DN_K + 1) + DN_CHUNK * (DN_CHUNK + 1) + 2 * DN_CHUNK * SCAN_VW + DN_K * SCAN_VW + 2 * DN_CHUNK) * 4;
+constexpr int SCAN_THREADS = 512;
+constexpr int SCAN_LDK = DN_K + 4, SCAN_LDA = DN_CHUNK + 4;       // padded rows: 16-byte aligned and conflict-free
+constexpr int CHUNK_SCAN_SMEM = (3 * DN_CHUNK * SCAN_LDK + DN_CHUNK * SCAN_LDA + 2 * DN_CHUNK * SCAN_VW + DN_K * SCAN_VW) * 4;
 
-static __global__ void __launch_bounds__(256) pf_dn_chunk_scan_kernel(const bf16* __restrict__ qkv, const ChunkScratch* __restrict__ scratch,
-                                                               bf16* __restrict__ core_out, float* __restrict__ state_out,
-                                                               int S, int nchunks) {
-    extern __shared__ float sm[];
-    float (*skcd)[DN_K + 1] = reinterpret_cast<float (*)[DN_K + 1]>(sm);
-    float (*sq)[DN_K + 1] = reinterpret_cast<float (*)[DN_K + 1]>(sm + DN_CHUNK * (DN_K + 1));      // q * scale * exp(gc_i)
-    float (*sk)[DN_K + 1] = reinterpret_cast<float (*)[DN_K + 1]>(sm + 2 * DN_CHUNK * (DN_K + 1));  // k * exp(gc_last - gc_i)
-    float (*sa)[DN_CHUNK + 1] = reinterpret_cast<float (*)[DN_CHUNK + 1]>(sm + 3 * DN_CHUNK * (DN_K + 1));
-    float (*svp)[SCAN_VW] = reinterpret_cast<float (*)[SCAN_VW]>(sm + 3 * DN_CHUNK * (DN_K + 1) + DN_CHUNK * (DN_CHUNK + 1));
-    float (*svn)[SCAN_VW] = svp + DN_CHUNK;
-    float (*sst)[SCAN_VW] = svn + DN_CHUNK;                    // state slice [k][v]
-    float* sgc = reinterpret_cast<float*>(sst + DN_K);
-    float* seg = sgc + DN_CHUNK;
-    const int h = blockIdx.x, vs = blockIdx.y, tid = threadIdx.x;
+__device__ __forceinline__ void scan_cp16(float* dst, const float* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src) : "memory");
+}
+
+static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(const ChunkScratch* __restrict__ scratch, bf16* __restrict__ core_out,
+                                                                        float* __restrict__ state_out, int S, int nchunks) {
+    extern __shared__ __align__(16) float sm[];
+    float* skcd = sm;                                   // [64][SCAN_LDK]
+    float* sq = skcd + DN_CHUNK * SCAN_LDK;             // [64][SCAN_LDK]
+    float* sk = sq + DN_CHUNK * SCAN_LDK;               // [64][SCAN_LDK]
+    float* sa = sk + DN_CHUNK * SCAN_LDK;               // [64][SCAN_LDA]
+    float* svp = sa + DN_CHUNK * SCAN_LDA;              // [64][16]
+    float* svn = svp + DN_CHUNK * SCAN_VW;              // [64][16]
+    float* sst = svn + DN_CHUNK * SCAN_VW;              // [128][16] state slice [k][v]
+    const int h = blockIdx.x, vs = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
     const int v0 = vs * SCAN_VW;
-    for (int e = tid; e < DN_K * SCAN_VW; e += 256) sst[e / SCAN_VW][e % SCAN_VW] = 0.f;
+    for (int e = tid; e < DN_K * SCAN_VW; e += SCAN_THREADS) sst[e] = 0.f;
+
+    auto issue_g1 = [&](int c) {
+        if (c < nchunks) {
+            const ChunkScratch& in = scratch[(size_t)h * nchunks + c];
+            for (int e = tid; e < DN_CHUNK * (DN_K / 4); e += SCAN_THREADS) {
+                const int i = e >> 5, q4 = (e & 31) * 4;
+                scan_cp16(skcd + i * SCAN_LDK + q4, &in.kcd[i][q4]);
+                scan_cp16(sq + i * SCAN_LDK + q4, &in.qs[i][q4]);
+            }
+            for (int e = tid; e < DN_CHUNK * (SCAN_VW / 4); e += SCAN_THREADS) {
+                const int i = e >> 2, q4 = (e & 3) * 4;
+                scan_cp16(svp + i * SCAN_VW + q4, &in.vprime[i][v0 + q4]);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    auto issue_g2 = [&](int c) {
+        if (c < nchunks) {
+            const ChunkScratch& in = scratch[(size_t)h * nchunks + c];
+            for (int e = tid; e < DN_CHUNK * (DN_K / 4); e += SCAN_THREADS) {
+                const int i = e >> 5, q4 = (e & 31) * 4;
+                scan_cp16(sk + i * SCAN_LDK + q4, &in.ks[i][q4]);
+            }
+            for (int e = tid; e < DN_CHUNK * (DN_CHUNK / 4); e += SCAN_THREADS) {
+                const int i = e >> 4, q4 = (e & 15) * 4;
+                scan_cp16(sa + i * SCAN_LDA + q4, &in.aqk[i][q4]);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    issue_g1(0);
+    issue_g2(0);
 
     for (int c = 0; c < nchunks; ++c) {
-        const ChunkScratch& in = scratch[(size_t)h * nchunks + c];
         const int t0 = c * DN_CHUNK;
+        const float dec = scratch[(size_t)h * nchunks + c].eg_last[0];
+        asm volatile("cp.async.wait_group 1;" ::: "memory");          // group 1 of this chunk has landed
         __syncthreads();
-        const float g_last = in.gc[DN_CHUNK - 1];
-        if (tid < DN_CHUNK) { const float gv = in.gc[tid]; sgc[tid] = expf(g_last - gv); seg[tid] = expf(gv); }
-        __syncthreads();
-        for (int e = tid; e < DN_CHUNK * DN_K; e += 256) {
-            const int i = e >> 7, d = e & 127, t = t0 + i;
-            float qv = 0.f, kv = 0.f;
-            if (t < S) {
-                const bf16* row = qkv + (size_t)t * DN_CONV_CH + h * DN_K + d;
-                qv = bf2f(row[0]) * 0.08838834764831845f;
-                kv = bf2f(row[DN_QK_SIZE]);
-            }
-            skcd[i][d] = in.kcd[i][d];
-            sq[i][d] = qv * seg[i];
-            sk[i][d] = kv * sgc[i];
-        }
-        for (int e = tid; e < DN_CHUNK * DN_CHUNK; e += 256) sa[e >> 6][e & 63] = in.aqk[e >> 6][e & 63];
-        for (int e = tid; e < DN_CHUNK * SCAN_VW; e += 256) svp[e / SCAN_VW][e % SCAN_VW] = in.vprime[e / SCAN_VW][v0 + e % SCAN_VW];
-        __syncthreads();
-        // v_new = vprime - kcd @ S ;  inter = (q exp gc) @ S      thread: row i = tid / 4, four value columns
-        const int i = tid >> 2, vq = (tid & 3) * 4;
+        // phase 1: v_new = vprime - kcd S ; inter = qs S.   thread: row i, four value columns, half of the key range
+        const int i = tid >> 3, vq = ((tid >> 1) & 3) * 4, kh = tid & 1;
         float vp[4] = {0.f, 0.f, 0.f, 0.f}, it[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int d = 0; d < DN_K; ++d) {
-            const float4 s4 = *reinterpret_cast<const float4*>(&sst[d][vq]);
-            const float a = skcd[i][d], b = sq[i][d];
-            vp[0] = fmaf(a, s4.x, vp[0]); vp[1] = fmaf(a, s4.y, vp[1]); vp[2] = fmaf(a, s4.z, vp[2]); vp[3] = fmaf(a, s4.w, vp[3]);
-            it[0] = fmaf(b, s4.x, it[0]); it[1] = fmaf(b, s4.y, it[1]); it[2] = fmaf(b, s4.z, it[2]); it[3] = fmaf(b, s4.w, it[3]);
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) svn[i][vq + u] = svp[i][vq + u] - vp[u];
-        __syncthreads();
-        // out = inter + aqk @ v_new
         {
-            float o[4] = {it[0], it[1], it[2], it[3]};
-            for (int j = 0; j <= i; ++j) {
-                const float a = sa[i][j];
-                const float4 n4 = *reinterpret_cast<const float4*>(&svn[j][vq]);
+            const float* ar = skcd + i * SCAN_LDK + kh;                 // keys kh, kh + 2, ...: the two halves hit different banks
+            const float* br = sq + i * SCAN_LDK + kh;
+            const float* sr = sst + kh * SCAN_VW + vq;
+#pragma unroll 8
+            for (int d = 0; d < DN_K / 2; ++d) {
+                const float4 s4 = *reinterpret_cast<const float4*>(sr + 2 * d * SCAN_VW);
+                const float a = ar[2 * d], b = br[2 * d];
+                vp[0] = fmaf(a, s4.x, vp[0]); vp[1] = fmaf(a, s4.y, vp[1]); vp[2] = fmaf(a, s4.z, vp[2]); vp[3] = fmaf(a, s4.w, vp[3]);
+                it[0] = fmaf(b, s4.x, it[0]); it[1] = fmaf(b, s4.y, it[1]); it[2] = fmaf(b, s4.z, it[2]); it[3] = fmaf(b, s4.w, it[3]);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                vp[u] += __shfl_xor_sync(0xffffffffu, vp[u], 1);
+                it[u] += __shfl_xor_sync(0xffffffffu, it[u], 1);
+            }
+            if (kh == 0) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) svn[i * SCAN_VW + vq + u] = svp[i * SCAN_VW + vq + u] - vp[u];
+            }
+        }
+        __syncthreads();                                               // v_new complete; kcd / qs / vprime buffers are free
+        issue_g1(c + 1);
+        asm volatile("cp.async.wait_group 1;" ::: "memory");          // group 2 of this chunk has landed
+        __syncthreads();
+        // phase 2: out = inter + aqk v_new   (the two key-halves of a row split the j range)
+        {
+            float o[4] = {0.f, 0.f, 0.f, 0.f};
+            const float* ar = sa + i * SCAN_LDA;
+            for (int j = kh; j <= i; j += 2) {
+                const float a = ar[j];
+                const float4 n4 = *reinterpret_cast<const float4*>(svn + j * SCAN_VW + vq);
                 o[0] = fmaf(a, n4.x, o[0]); o[1] = fmaf(a, n4.y, o[1]); o[2] = fmaf(a, n4.z, o[2]); o[3] = fmaf(a, n4.w, o[3]);
             }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) o[u] += __shfl_xor_sync(0xffffffffu, o[u], 1);
             const int t = t0 + i;
-            if (t < S) {
+            if (kh == 0 && t < S) {
                 bf16* dst = core_out + (size_t)t * DN_V_SIZE + h * DN_V + v0 + vq;
-                *reinterpret_cast<__nv_bfloat162*>(dst) = __halves2bfloat162(f2bf(o[0]), f2bf(o[1]));
-                *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __halves2bfloat162(f2bf(o[2]), f2bf(o[3]));
+                *reinterpret_cast<__nv_bfloat162*>(dst) = __halves2bfloat162(f2bf(it[0] + o[0]), f2bf(it[1] + o[1]));
+                *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __halves2bfloat162(f2bf(it[2] + o[2]), f2bf(it[3] + o[3]));
             }
         }
-        // S = S * exp(g_last) + (k exp(g_last - gc))^T @ v_new       thread: key d = tid / 2, eight value columns
+        // phase 3: S = S exp(gc_last) + ks^T v_new.   thread: key d, four value columns
         {
-            const int d = tid >> 1, vo = (tid & 1) * 8;
-            float acc[8];
-            const float dec = expf(g_last);
-#pragma unroll
-            for (int u = 0; u < 8; ++u) acc[u] = sst[d][vo + u] * dec;
+            const int d = tid >> 2, vo = (tid & 3) * 4;
+            float acc[4];
+            const float4 s4 = *reinterpret_cast<const float4*>(sst + d * SCAN_VW + vo);
+            acc[0] = s4.x * dec; acc[1] = s4.y * dec; acc[2] = s4.z * dec; acc[3] = s4.w * dec;
+#pragma unroll 8
             for (int j = 0; j < DN_CHUNK; ++j) {
-                const float kw = sk[j][d];
-                const float4 n0 = *reinterpret_cast<const float4*>(&svn[j][vo]);
-                const float4 n1 = *reinterpret_cast<const float4*>(&svn[j][vo + 4]);
-                acc[0] = fmaf(kw, n0.x, acc[0]); acc[1] = fmaf(kw, n0.y, acc[1]); acc[2] = fmaf(kw, n0.z, acc[2]); acc[3] = fmaf(kw, n0.w, acc[3]);
-                acc[4] = fmaf(kw, n1.x, acc[4]); acc[5] = fmaf(kw, n1.y, acc[5]); acc[6] = fmaf(kw, n1.z, acc[6]); acc[7] = fmaf(kw, n1.w, acc[7]);
+                const float kw = sk[j * SCAN_LDK + d];
+                const float4 n4 = *reinterpret_cast<const float4*>(svn + j * SCAN_VW + vo);
+                acc[0] = fmaf(kw, n4.x, acc[0]); acc[1] = fmaf(kw, n4.y, acc[1]); acc[2] = fmaf(kw, n4.z, acc[2]); acc[3] = fmaf(kw, n4.w, acc[3]);
             }
-            __syncthreads();       // everyone has finished reading the old state
-#pragma unroll
-            for (int u = 0; u < 8; ++u) sst[d][vo + u] = acc[u];
+            // each thread reads and writes only its own four state words here; phase 1 of the next chunk reads them
+            // all, after the barrier at the top of the loop
+            *reinterpret_cast<float4*>(sst + d * SCAN_VW + vo) = make_float4(acc[0], acc[1], acc[2], acc[3]);
         }
+        __syncthreads();                                               // aqk / ks buffers are free
+        issue_g2(c + 1);
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
     // final state in the reference layout [head][v][k]
-    for (int e = tid; e < DN_K * SCAN_VW; e += 256) {
+    for (int e = tid; e < DN_K * SCAN_VW; e += SCAN_THREADS) {
         const int v = e / DN_K, d = e % DN_K;
-        state_out[((size_t)h * DN_V + v0 + v) * DN_K + d] = sst[d][v];
+        state_out[((size_t)h * DN_V + v0 + v) * DN_K + d] = sst[d * SCAN_VW + v];
     }
+    (void)lane;
 }
 
 // ---- gated RMSNorm of the DeltaNet output: one warp per (token, head) --------------------------------
