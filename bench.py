@@ -195,10 +195,11 @@ def batched_decode_bench(weights_gpu, dev, rank, n_seq, ctx, n_steps, kernel_tab
     prefill, `n_steps` greedy steps.  Returns (tok/s on this rank, ms per step, algorithmic bytes per step)."""
     from qwen35_b200.config import QWEN35_0P8B as D
     from qwen35_b200.model import BatchedDecoder
+    from qwen35_b200.sharding import sequence_seed
     from qwen35_b200.weights import make_token_ids
     bd = BatchedDecoder(weights_gpu, batch=n_seq, max_ctx=ctx + n_steps + 64, device=dev)
     for sq in range(n_seq):
-        bd.prefill(sq, make_token_ids(ctx, 1000 * rank + sq, D.vocab).to(dev))
+        bd.prefill(sq, make_token_ids(ctx, sequence_seed(0, rank, sq), D.vocab).to(dev))
     snap = [t.clone() for t in (bd.dn_states, bd.conv_bufs, bd.positions, bd.tokens)]
     for _ in range(3):
         bd.step(graph=True)
@@ -417,12 +418,10 @@ def run_ours(args):
     batched = None
     if args.batched > 0:
         b_tok_s, b_ms, b_bytes = batched_decode_bench(wg, dev, rank, args.batched, args.batched_ctx, GEN, kernel_table=args.kernel_table and rank == 0)
-        bt = torch.tensor([b_tok_s, b_ms], dtype=torch.float64, device=dev)
-        if world > 1:
-            import torch.distributed as dist
-            tmin = bt.clone(); dist.all_reduce(tmin, op=dist.ReduceOp.MIN)
-            tmax = bt.clone(); dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
-            b_tok_s, b_ms = float(tmin[0]), float(tmax[1])
+        from qwen35_b200.sharding import reduce_counters
+        job = reduce_counters(tokens=args.batched * GEN, elapsed_ms=b_ms * GEN, algorithmic_bytes=b_bytes * GEN, device=dev)
+        b_ms = job.elapsed_ms / GEN                         # slowest rank's time per step
+        b_tok_s = job.tokens_per_s / world                  # per-GPU rate of the whole job
         batched = {"workload": "BASELINE configs[3]: %d sequences per GPU, %d-token contexts, %d greedy steps, no collectives" % (args.batched, args.batched_ctx, GEN),
                    "value": world * b_tok_s, "unit": "tok/s", "per_gpu_tok_s": b_tok_s, "ms_per_step": b_ms,
                    "algorithmic_bytes_per_step": b_bytes, "hbm_gbs": b_bytes / (b_ms * 1e-3) / 1e9,
