@@ -45,14 +45,18 @@ LAYER_TYPE = _D.layer_types
 
 
 def load_weights(model_name="random:1234", verbose=True, backend="bf16", device="cuda"):
-    """Reference signature (model.py:314-319).  Only `random:<seed>` sources exist here: no
-    checkpoint can be downloaded where this runs.  Returns (weights, tokenizer=None)."""
-    from .weights import make_random_weights, weights_to
-    if not str(model_name).startswith("random:"):
-        raise NotImplementedError(
-            "checkpoint loading needs files that are not available here; use 'random:<seed>'")
-    w = make_random_weights(int(str(model_name).split(":", 1)[1]), _D)
-    return weights_to(w, device), None
+    """Reference signature (model.py:314-319).  `random:<seed>` gives the seeded random-init weights; a path to a
+    HuggingFace checkpoint directory or `.safetensors` file is read directly (no network, no tokenizer: the second
+    return value is None).  A hub id cannot be resolved where this runs."""
+    import os
+
+    from .weights import load_safetensors_weights, make_random_weights, weights_to
+    name = str(model_name)
+    if name.startswith("random:"):
+        return weights_to(make_random_weights(int(name.split(":", 1)[1]), _D), device), None
+    if os.path.exists(name):
+        return load_safetensors_weights(name, _D, device), None
+    raise FileNotFoundError(f"{name}: not 'random:<seed>' and not a local checkpoint path (no hub download is possible here)")
 
 
 NVFP4_GROUP_SIZE = 32
