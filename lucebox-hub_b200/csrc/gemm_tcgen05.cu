@@ -663,7 +663,9 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
     GemmParams p{M, N, K, C, ldc, R, ldr, up_row_offset, (int*)ws};
     const int bn_out = (epi == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
     const int m_tiles = (M + GEMM_BM - 1) / GEMM_BM, n_tiles = (N + bn_out - 1) / bn_out, nkb = K / GEMM_BK;
-    if (m_tiles > 1) {
+    // a grid that cannot fill the SMs (few tiles, long K) also splits K over clusters
+    const bool small_grid = m_tiles * n_tiles < 100 && nkb >= 8;
+    if (m_tiles > 1 && !small_grid) {
         dim3 grid(n_tiles, m_tiles);
 #define Q35_GEMM_WIDE(E)                                                                                                                      \
     case E: {                                                                                                                                 \
@@ -679,11 +681,11 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
         switch (epi) { Q35_GEMM_WIDE(EPI_BF16) Q35_GEMM_WIDE(EPI_RESIDUAL) Q35_GEMM_WIDE(EPI_SILU_MUL) }
 #undef Q35_GEMM_WIDE
     } else {
-        // one row of tiles: split K over a cluster until about one CTA per SM exists, at least two k-steps per CTA
+        // few tiles: split K over a cluster until about one CTA per SM exists, at least two k-steps per CTA
         int split = 1;
-        while (split < GEMM_MAX_SPLIT && n_tiles * split < 120 && nkb / (split * 2) >= 2) split *= 2;
+        while (split < GEMM_MAX_SPLIT && m_tiles * n_tiles * split < 120 && nkb / (split * 2) >= 2) split *= 2;
         if (split == 1) {
-            dim3 grid(n_tiles, 1);
+            dim3 grid(n_tiles, m_tiles);
 #define Q35_GEMM_ROW(E)                                                                                                                         \
     case E: {                                                                                                                                   \
         static bool attr = false;                                                                                                               \
@@ -702,7 +704,7 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
             return QWEN35_OK;
         }
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(n_tiles, 1, split);
+        cfg.gridDim = dim3(n_tiles, m_tiles, split);
         cfg.blockDim = dim3(GEMM_THREADS);
         cfg.dynamicSmemBytes = gemm_smem(GEMM_STAGES_SKINNY);
         cfg.stream = stream;

@@ -99,7 +99,7 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
             pf_dn_prep_kernel<<<dim3(S, DN_HEADS), 128, 0, stream>>>(a.proj_buf, ldp, (const bf16*)L.p[DN_CONV], (const bf16*)L.p[DN_ALOG],
                                                                       (const bf16*)L.p[DN_DTBIAS], a.proj_buf2, a.beta_buf, a.alpha_buf, S);
             pf_conv_state_kernel<<<(DN_CONV_CH + 255) / 256, 256, 0, stream>>>(a.proj_buf, ldp, a.conv_bufs + (size_t)i_dn * DN_CONV_CH * 4, S);
-            pf_dn_chunk_local_kernel<<<dim3(nchunks, DN_HEADS), 256, CHUNK_LOCAL_SMEM, stream>>>(a.proj_buf2, a.beta_buf, a.alpha_buf, scratch, S, nchunks);
+            pf_dn_chunk_local_kernel<<<dim3(nchunks, DN_HEADS), CL_THREADS, CHUNK_LOCAL_SMEM, stream>>>(a.proj_buf2, a.beta_buf, a.alpha_buf, scratch, S, nchunks);
             pf_dn_chunk_scan_kernel<<<dim3(DN_HEADS, DN_V / SCAN_VW), SCAN_THREADS, CHUNK_SCAN_SMEM, stream>>>(
                 scratch, a.dn_out_buf, a.dn_states + (size_t)i_dn * DN_HEADS * DN_V * DN_K, S, nchunks);
             pf_gated_norm_kernel<<<(S * DN_HEADS + 7) / 8, 256, 0, stream>>>(a.dn_out_buf, a.proj_buf, ldp, (const bf16*)L.p[DN_NORM], a.attn_buf, S);

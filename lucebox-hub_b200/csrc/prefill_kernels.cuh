@@ -132,17 +132,24 @@ struct ChunkScratch {          // one record per (head, chunk), floats; every ar
     float eg_last[4];              // [0] = exp(gc_last)
 };
 
-constexpr int CHUNK_LOCAL_SMEM = (2 * DN_CHUNK * (DN_K + 1) + DN_CHUNK * DN_V + DN_CHUNK * (DN_CHUNK + 1) + 3 * DN_CHUNK) * 4;
+constexpr int CL_THREADS = 512;
+constexpr int CL_LD = DN_K + 4;                          // padded rows: float4 loads, conflict-free for rows 16 apart
+constexpr int CL_LDA = DN_CHUNK + 1;
+constexpr int CHUNK_LOCAL_SMEM = (3 * DN_CHUNK * CL_LD + DN_CHUNK * CL_LDA + 3 * DN_CHUNK) * 4;
 
-static __global__ void __launch_bounds__(256) pf_dn_chunk_local_kernel(const bf16* __restrict__ qkv, const float* __restrict__ beta,
-                                                                const float* __restrict__ g, ChunkScratch* __restrict__ scratch,
-                                                                int S, int nchunks) {
-    extern __shared__ float sm[];
-    float (*sq)[DN_K + 1] = reinterpret_cast<float (*)[DN_K + 1]>(sm);                       // q * 1/sqrt(128)
-    float (*sk)[DN_K + 1] = reinterpret_cast<float (*)[DN_K + 1]>(sm + DN_CHUNK * (DN_K + 1));
-    float (*sv)[DN_V] = reinterpret_cast<float (*)[DN_V]>(sm + 2 * DN_CHUNK * (DN_K + 1));     // v * beta
-    float (*sa)[DN_CHUNK + 1] = reinterpret_cast<float (*)[DN_CHUNK + 1]>(sm + 2 * DN_CHUNK * (DN_K + 1) + DN_CHUNK * DN_V);
-    float* sb = sm + 2 * DN_CHUNK * (DN_K + 1) + DN_CHUNK * DN_V + DN_CHUNK * (DN_CHUNK + 1);
+__device__ __forceinline__ float dot4(const float4 a, const float4 b, float acc) {
+    acc = fmaf(a.x, b.x, acc); acc = fmaf(a.y, b.y, acc); acc = fmaf(a.z, b.z, acc); return fmaf(a.w, b.w, acc);
+}
+
+static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(const bf16* __restrict__ qkv, const float* __restrict__ beta,
+                                                                       const float* __restrict__ g, ChunkScratch* __restrict__ scratch,
+                                                                       int S, int nchunks) {
+    extern __shared__ __align__(16) float sm[];
+    float* sq = sm;                                  // [64][CL_LD]  q / sqrt(128); later k * beta * exp(gc)
+    float* sk = sq + DN_CHUNK * CL_LD;               // [64][CL_LD]  k
+    float* sv = sk + DN_CHUNK * CL_LD;               // [64][CL_LD]  v * beta
+    float* sa = sv + DN_CHUNK * CL_LD;               // [64][CL_LDA]
+    float* sb = sa + DN_CHUNK * CL_LDA;
     float* sg = sb + DN_CHUNK;      // cumulative log-decay
     float* se = sg + DN_CHUNK;      // exp(gc)
     const int c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
@@ -154,7 +161,7 @@ static __global__ void __launch_bounds__(256) pf_dn_chunk_local_kernel(const bf1
         sb[tid] = (t < S) ? beta[t * DN_HEADS + h] : 0.f;
         sg[tid] = (t < S) ? g[t * DN_HEADS + h] : 0.f;
     }
-    for (int e = tid; e < DN_CHUNK * DN_K; e += 256) {
+    for (int e = tid; e < DN_CHUNK * DN_K; e += CL_THREADS) {
         const int i = e >> 7, d = e & 127, t = t0 + i;
         float qv = 0.f, kv = 0.f, vv = 0.f;
         if (t < S) {
@@ -163,7 +170,7 @@ static __global__ void __launch_bounds__(256) pf_dn_chunk_local_kernel(const bf1
             kv = bf2f(row[DN_QK_SIZE]);
             vv = bf2f(row[2 * DN_QK_SIZE]);
         }
-        sq[i][d] = qv; sk[i][d] = kv; sv[i][d] = vv;
+        sq[i * CL_LD + d] = qv; sk[i * CL_LD + d] = kv; sv[i * CL_LD + d] = vv;
     }
     __syncthreads();
     if (tid == 0) {                 // sequential cumsum, as torch.cumsum does
@@ -172,54 +179,110 @@ static __global__ void __launch_bounds__(256) pf_dn_chunk_local_kernel(const bf1
     }
     __syncthreads();
     if (tid < DN_CHUNK) { se[tid] = expf(sg[tid]); out.gc[tid] = sg[tid]; }
-    for (int e = tid; e < DN_CHUNK * DN_V; e += 256) sv[e >> 7][e & 127] *= sb[e >> 7];      // v * beta
+    for (int e = tid; e < DN_CHUNK * DN_V; e += CL_THREADS) sv[(e >> 7) * CL_LD + (e & 127)] *= sb[e >> 7];      // v * beta
     __syncthreads();
     {   // operands of the scan that depend on this chunk only
         const float g_last = sg[DN_CHUNK - 1];
-        for (int e = tid; e < DN_CHUNK * DN_K; e += 256) {
+        for (int e = tid; e < DN_CHUNK * DN_K; e += CL_THREADS) {
             const int i = e >> 7, d = e & 127;
-            out.qs[i][d] = sq[i][d] * se[i];
-            out.ks[i][d] = sk[i][d] * expf(g_last - sg[i]);
+            out.qs[i][d] = sq[i * CL_LD + d] * se[i];
+            out.ks[i][d] = sk[i * CL_LD + d] * expf(g_last - sg[i]);
         }
         if (tid == 0) out.eg_last[0] = expf(g_last);
     }
     // A[i][j] = -(beta_i k_i . k_j) * exp(gc_i - gc_j) for j < i, else 0;   aqk[i][j] = (q_i . k_j) * exp(gc_i - gc_j) for j <= i
-    for (int e = tid; e < DN_CHUNK * DN_CHUNK; e += 256) {
-        const int i = e >> 6, j = e & 63;
-        float kk = 0.f, qk = 0.f;
-        if (j <= i) {
-            for (int d = 0; d < DN_K; ++d) { kk = fmaf(sk[i][d] * sb[i], sk[j][d], kk); qk = fmaf(sq[i][d], sk[j][d], qk); }
+    // register tile per thread: rows bi, bi + 32 x columns bj, bj + 16, bj + 32, bj + 48 (rows 16 apart: conflict-free float4 loads)
+    {
+        const int bi = tid >> 4, bj = tid & 15;
+        float kk[2][4], qk[2][4];
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) { kk[r][cc] = 0.f; qk[r][cc] = 0.f; }
+#pragma unroll 2
+        for (int d = 0; d < DN_K; d += 4) {
+            float4 ki[2], qi[2], kj[4];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                ki[r] = *reinterpret_cast<const float4*>(sk + (bi + 32 * r) * CL_LD + d);
+                qi[r] = *reinterpret_cast<const float4*>(sq + (bi + 32 * r) * CL_LD + d);
+            }
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) kj[cc] = *reinterpret_cast<const float4*>(sk + (bj + 16 * cc) * CL_LD + d);
+#pragma unroll
+            for (int r = 0; r < 2; ++r)
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) { kk[r][cc] = dot4(ki[r], kj[cc], kk[r][cc]); qk[r][cc] = dot4(qi[r], kj[cc], qk[r][cc]); }
         }
-        const float dec = (j <= i) ? expf(sg[i] - sg[j]) : 0.f;
-        sa[i][j] = (j < i) ? -(kk * dec) : 0.f;
-        out.aqk[i][j] = (j <= i) ? qk * dec : 0.f;
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                const int i = bi + 32 * r, j = bj + 16 * cc;
+                const float dec = (j <= i) ? expf(sg[i] - sg[j]) : 0.f;
+                sa[i * CL_LDA + j] = (j < i) ? -((kk[r][cc] * sb[i]) * dec) : 0.f;
+                out.aqk[i][j] = (j <= i) ? qk[r][cc] * dec : 0.f;
+            }
     }
     __syncthreads();
-    // forward substitution, row by row: row_i[:i] += sum_{j<i} row_i[j] * A[j][:i]  (rows j < i already final)
-    for (int i = 1; i < DN_CHUNK; ++i) {
-        float nv = 0.f;
-        if (tid < i) {
-            float acc = 0.f;
-            for (int j = 0; j < i; ++j) acc += sa[i][j] * sa[j][tid];
-            nv = sa[i][tid] + acc;
-        }
-        __syncthreads();
-        if (tid < i) sa[i][tid] = nv;
-        __syncthreads();
-    }
-    if (tid < DN_CHUNK) sa[tid][tid] = 1.0f;
-    __syncthreads();
-    // vprime = T (v beta);  kcd = T (k beta exp(gc))
-    for (int e = tid; e < DN_CHUNK * DN_V; e += 256) {
+    // k * beta * exp(gc) replaces q (no longer needed)
+    for (int e = tid; e < DN_CHUNK * DN_K; e += CL_THREADS) {
         const int i = e >> 7, d = e & 127;
-        float a0 = 0.f, a1 = 0.f;
-        for (int j = 0; j <= i; ++j) {
-            const float tv = sa[i][j];
-            a0 = fmaf(tv, sv[j][d], a0);
-            a1 = fmaf(tv, (sk[j][d] * sb[j]) * se[j], a1);
+        sq[i * CL_LD + d] = (sk[i * CL_LD + d] * sb[i]) * se[i];
+    }
+    // forward substitution, row by row: row_i[:i] += sum_{j<i} row_i[j] * A[j][:i]  (rows j < i already final).
+    // Only 64 threads take part, so the 126 hand-offs use a 64-thread named barrier; the other warps wait below.
+    if (tid < DN_CHUNK) {
+        for (int i = 1; i < DN_CHUNK; ++i) {
+            float nv = 0.f;
+            if (tid < i) {
+                // four independent partial sums keep four pairs of shared-memory loads in flight
+                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+                const float* ri = sa + i * CL_LDA;
+                const float* cj = sa + tid;
+                int j = 0;
+                for (; j + 4 <= i; j += 4) {
+                    a0 = fmaf(ri[j], cj[j * CL_LDA], a0);
+                    a1 = fmaf(ri[j + 1], cj[(j + 1) * CL_LDA], a1);
+                    a2 = fmaf(ri[j + 2], cj[(j + 2) * CL_LDA], a2);
+                    a3 = fmaf(ri[j + 3], cj[(j + 3) * CL_LDA], a3);
+                }
+                for (; j < i; ++j) a0 = fmaf(ri[j], cj[j * CL_LDA], a0);
+                nv = ri[tid] + ((a0 + a1) + (a2 + a3));
+            }
+            asm volatile("bar.sync 1, 64;" ::: "memory");
+            if (tid < i) sa[i * CL_LDA + tid] = nv;
+            asm volatile("bar.sync 1, 64;" ::: "memory");
         }
-        out.vprime[i][d] = a0;
-        out.kcd[i][d] = a1;
+    }
+    __syncthreads();
+    if (tid < DN_CHUNK) sa[tid * CL_LDA + tid] = 1.0f;
+    __syncthreads();
+    // vprime = T (v beta);  kcd = T (k beta exp(gc)).  thread: four columns, rows ig, ig + 16, ig + 32, ig + 48; T is zero above
+    // its diagonal, so every row runs over the same j range
+    {
+        const int d4 = (tid & 31) * 4, ig = tid >> 5;
+        float av[4][4], ak[4][4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r)
+#pragma unroll
+            for (int u = 0; u < 4; ++u) { av[r][u] = 0.f; ak[r][u] = 0.f; }
+        const int jmax = ig + 48;
+        for (int j = 0; j <= jmax; ++j) {
+            const float4 v4 = *reinterpret_cast<const float4*>(sv + j * CL_LD + d4);
+            const float4 k4 = *reinterpret_cast<const float4*>(sq + j * CL_LD + d4);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                const float tv = sa[(ig + 16 * r) * CL_LDA + j];
+                av[r][0] = fmaf(tv, v4.x, av[r][0]); av[r][1] = fmaf(tv, v4.y, av[r][1]); av[r][2] = fmaf(tv, v4.z, av[r][2]); av[r][3] = fmaf(tv, v4.w, av[r][3]);
+                ak[r][0] = fmaf(tv, k4.x, ak[r][0]); ak[r][1] = fmaf(tv, k4.y, ak[r][1]); ak[r][2] = fmaf(tv, k4.z, ak[r][2]); ak[r][3] = fmaf(tv, k4.w, ak[r][3]);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            *reinterpret_cast<float4*>(&out.vprime[ig + 16 * r][d4]) = make_float4(av[r][0], av[r][1], av[r][2], av[r][3]);
+            *reinterpret_cast<float4*>(&out.kcd[ig + 16 * r][d4]) = make_float4(ak[r][0], ak[r][1], ak[r][2], ak[r][3]);
+        }
     }
 }
 
