@@ -17,6 +17,7 @@
 // applies the epilogue.  No partial sums go through global memory and no second kernel runs.
 // Every wait is bounded; a wait that runs out sets the status word and the CTA unwinds normally.
 #include <cuda.h>
+#include <cstdlib>
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -665,7 +666,25 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
     const int m_tiles = (M + GEMM_BM - 1) / GEMM_BM, n_tiles = (N + bn_out - 1) / bn_out, nkb = K / GEMM_BK;
     // a grid that cannot fill the SMs (few tiles, long K) also splits K over clusters
     const bool small_grid = m_tiles * n_tiles < 100 && nkb >= 8;
-    if (m_tiles > 1 && !small_grid) {
+    // more tiles than SMs: 3 stages per CTA let two CTAs share an SM (the same bytes in flight per SM as 6 stages of one
+    // CTA), so the prologue / epilogue of one tile overlaps the main loop of another
+    const bool two_per_sm = m_tiles > 1 && !small_grid && m_tiles * n_tiles > 148;
+    if (two_per_sm) {
+        dim3 grid(n_tiles, m_tiles);
+#define Q35_GEMM_ROW2(E)                                                                                                                        \
+    case E: {                                                                                                                                   \
+        static bool attr = false;                                                                                                               \
+        if (!attr) {                                                                                                                            \
+            Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                             (int)gemm_smem(GEMM_STAGES_SKINNY)));                                                              \
+            attr = true;                                                                                                                        \
+        }                                                                                                                                       \
+        gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, false><<<grid, GEMM_THREADS, gemm_smem(GEMM_STAGES_SKINNY), stream>>>(tmA, tmB, p);      \
+        break;                                                                                                                                  \
+    }
+        switch (epi) { Q35_GEMM_ROW2(EPI_BF16) Q35_GEMM_ROW2(EPI_RESIDUAL) Q35_GEMM_ROW2(EPI_SILU_MUL) }
+#undef Q35_GEMM_ROW2
+    } else if (m_tiles > 1 && !small_grid) {
         dim3 grid(n_tiles, m_tiles);
 #define Q35_GEMM_WIDE(E)                                                                                                                      \
     case E: {                                                                                                                                 \
