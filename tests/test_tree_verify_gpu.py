@@ -174,3 +174,28 @@ def test_tree_verify_argument_checks():
     tt.past = 250
     with pytest.raises(Qwen35Error):          # past + nodes beyond the cache
         tt.verify(torch.zeros(10, dtype=torch.int32), torch.tensor([-1] + list(range(9)), dtype=torch.int32))
+
+
+def test_gguf_loaded_target_equals_direct_weights(tmp_path):
+    """A target loaded from a GGUF file (reference tensor names) verifies a tree exactly like one built from the
+    same weights directly."""
+    pytest.importorskip("gguf")
+    from qwen35_b200.gguf_target import load_gguf_target, write_gguf_target
+    from qwen35_b200.tree_verify import TreeTarget, make_random_tree_weights, random_tree
+    D = small_dims()
+    w = make_random_tree_weights(D, 21)
+    path = str(tmp_path / "t.gguf")
+    write_gguf_target(path, D, w)
+    D2, w2 = load_gguf_target(path, device="cuda")
+    wg = {"layers": [{k: v.cuda() for k, v in L.items()} for L in w["layers"]],
+          "token_embd": w["token_embd"].cuda(), "output_norm": w["output_norm"].cuda(), "output_w": w["output_w"].cuda()}
+    tokens = torch.randint(0, D.vocab, (9,), dtype=torch.int32)
+    parents = torch.tensor(random_tree(9, 4, 2), dtype=torch.int32)
+    outs = []
+    for dims, weights in ((D, wg), (D2, w2)):
+        tt = TreeTarget(dims, weights, max_ctx=128)
+        lg = torch.zeros(9, D.vocab, dtype=torch.bfloat16, device="cuda")
+        am = tt.verify(tokens, parents, logits_out=lg).clone()
+        tt.check_status()
+        outs.append((am.cpu(), lg.cpu()))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
