@@ -286,6 +286,20 @@ int qwen35_b200_tree_commit(const Qwen35TreeVerifyArgs* args, const int* path, c
 /* Q4_K super-blocks -> f32 (bit-exact with the published dequantisation (d*sc)*q - dmin*m) and / or bf16. */
 int qwen35_b200_dequant_q4k(const void* blocks, size_t n_blocks, void* out_f32, void* out_bf16, qwen35_stream_t stream);
 
+/* Draft side of the speculative loop.  draft_topk: per position, the k largest logits / temperature as log-
+ * probabilities (log-sum-exp over the vocabulary) and their token ids, sorted by descending value and ascending id
+ * among equals, computed on the GPU (replaces the OpenMP pass extract_draft_topk, test_dflash.cpp:143-207).
+ * logits f32 [n_positions][vocab] on the device; outputs [n_positions][k] on the device; 1 <= k <= 16. */
+int qwen35_b200_draft_topk(const float* logits, int n_positions, int vocab, int k, float temperature, float* out_log_probs,
+                           int* out_token_ids, qwen35_stream_t stream);
+/* build_ddtree (test_dflash.cpp:218-390) on the host: best-first tree over prefixes of the per-depth top-k lists
+ * (HOST arrays [depth_max][k]), at most `budget` nodes beside the root, optional rank-0 chain first.  Outputs are HOST
+ * arrays of 1 + budget entries, node 0 = root (token -1, depth 0, parent -1), parents[i] < i; visibility (optional)
+ * is the (1+n)^2 ancestor-or-self matrix.  Returns the number of nodes beside the root, or -1 on bad arguments.  The
+ * token / parent arrays are what qwen35_b200_tree_verify takes (after the caller puts the root token in slot 0). */
+int qwen35_b200_build_ddtree(const float* top_log_probs, const int* top_token_ids, int depth_max, int k, int budget, int chain_seed,
+                             int* token_ids, int* depths, int* parents, unsigned char* visibility);
+
 /* The prefill and batched-decode entry points keep a host copy of the device pointer tables, keyed by the two
  * table addresses, exactly as the reference keeps its host copy (prefill.cu:1179-1195): after the first call they
  * neither synchronise nor allocate.  A caller that frees its tables and packs new ones may get the same addresses

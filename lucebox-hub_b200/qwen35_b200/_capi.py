@@ -97,6 +97,8 @@ SIGNATURES = {
     "launch_quantize_nvfp4_lm_out": (_i, [_vp, _i, _i, _vp, _vp, _vp]),
     "qwen35_b200_decode_batched": (_i, [C.POINTER(BatchedArgs), _vp]),
     "qwen35_b200_forget_tables": (None, []),
+    "qwen35_b200_draft_topk": (_i, [_vp, _i, _i, _i, C.c_float, _vp, _vp, _vp]),
+    "qwen35_b200_build_ddtree": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "qwen35_b200_tree_scratch_bytes": (C.c_size_t, [C.POINTER(TreeDimsC), _i, _i]),
     "qwen35_b200_tree_verify": (_i, [C.POINTER(TreeVerifyArgs), _vp]),
     "qwen35_b200_tree_accept": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp]),

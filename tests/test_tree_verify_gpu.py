@@ -199,3 +199,48 @@ def test_gguf_loaded_target_equals_direct_weights(tmp_path):
         tt.check_status()
         outs.append((am.cpu(), lg.cpu()))
     assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+
+
+@pytest.mark.parametrize("n,vocab,k,temp", [(5, 1000, 4, 1.0), (3, 248320, 8, 0.7), (1, 37, 16, 1.0)])
+def test_draft_topk_matches_oracle(n, vocab, k, temp):
+    from oracle.ddtree_oracle import draft_topk as oracle_topk
+    from qwen35_b200.ddtree import draft_topk
+    g = torch.Generator().manual_seed(n + vocab)
+    logits = (torch.randn(n, vocab, generator=g) * 4).float()
+    logits[0, 5] = logits[0, 11] = logits[0].max() + 1.0          # an exact tie at the top: the lower id comes first
+    lp, ids = draft_topk(logits.cuda(), k, temp)
+    rlp, rids = oracle_topk(logits.numpy(), k, temp)
+    assert torch.equal(ids.cpu(), torch.from_numpy(rids))
+    assert float((lp.cpu() - torch.from_numpy(rlp)).abs().max()) < 1e-4
+    assert int(ids[0, 0]) == 5 and int(ids[0, 1]) == 11
+
+
+def test_tree_verify_on_a_best_first_tree():
+    """The reference numbers tree nodes in best-first order (parents[i] < i but not DFS pre-order: the rank-0 chain
+    first, branches afterwards).  The pass must give the path-sequential result for that numbering too."""
+    from oracle.ddtree_oracle import draft_topk as oracle_topk
+    from qwen35_b200.ddtree import build_ddtree
+    D, orc, tt, rng = _setup(40, 6)
+    lp, ids = oracle_topk(rng.standard_normal((5, D.vocab)).astype(np.float32) * 2, 3)
+    tree = build_ddtree(lp, ids, budget=13, chain_seed=True)
+    tokens = tree.token_ids.copy(); tokens[0] = int(rng.integers(0, D.vocab))
+    parents = tree.parents.tolist()
+    assert any(parents[i] != i - 1 and parents[i] < i - 1 for i in range(1, len(parents)))      # really not a chain
+    ref_logits, ctxs, hids = orc.verify(tokens, parents)
+    n = len(parents)
+    teacher = torch.zeros(D.n_layers, n, D.hidden, dtype=torch.bfloat16)
+    for t in range(n):
+        for il in range(1, D.n_layers):
+            teacher[il, t] = hids[t][il - 1].bfloat16()
+    dbg = torch.zeros(D.n_layers, n, D.hidden, dtype=torch.bfloat16, device="cuda")
+    tt.verify(torch.tensor(tokens, dtype=torch.int32), torch.tensor(parents, dtype=torch.int32), dbg_hidden=dbg, dbg_teacher=teacher.cuda())
+    tt.check_status()
+    got = dbg.float().cpu()
+    for t in range(n):
+        for il in range(D.n_layers):
+            assert float((got[il, t] - hids[t][il]).abs().max()) <= LAYER_ABS_TOL, (t, il)
+    i_dn = [il for il in range(D.n_layers) if not D.is_fa(il)]
+    for t in range(n):
+        for j in range(len(i_dn)):
+            ref_s = ctxs[t]["ssm"][j]
+            assert float((tt.node_states[j, t].float().cpu() - ref_s).norm() / ref_s.norm().clamp_min(1e-6)) <= STATE_REL_TOL
