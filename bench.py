@@ -34,12 +34,12 @@ GEN = 128
 
 
 def workload_config(world: int) -> dict:
-    return {"workload": "qwen35-0.8b-arch random-init bf16, bs=1 per GPU, pp%d + tg%d greedy (BASELINE configs[0])" % (PROMPT, GEN),
+    return {"workload": "qwen35-0.8b-arch random-init bf16, bs=1 per GPU, pp%d + tg%d greedy (the reference's headline benchmark)" % (PROMPT, GEN),
             "prompt_tokens": PROMPT, "gen_tokens": GEN, "sequences_per_gpu": 1,
             "l2": "per-token working set 1.5 GB of weights >> 126 MB L2 (no flush needed)",
             "parallelism": f"replicas x{world}, no collectives"}
 
-BASELINE_TG128 = 711.0       # reference BF16 megakernel tg128 on B200
+BASELINE_TG128 = 711.0       # the reference's published BF16 megakernel tg128 on B200 (docs/results/qwen35_0p8b_b200.md)
 BASELINE_PP520 = 40278.0
 FALLBACK_HBM_GBS = 6650.0
 
@@ -123,7 +123,7 @@ def prefill_flops(S: int) -> float:
 
 
 def prefill_sweep(weights_gpu, dev, lengths):
-    """batched prefill at each prompt length (ids seed 7+S): 3 warm-up runs, 5 timed with CUDA
+    """Prefill sweep configuration: batched prefill at each prompt length (ids seed 7+S): 3 warm-up runs, 5 timed with CUDA
     events, best time reported with its share of the measured dense bf16 peak."""
     from qwen35_b200.config import QWEN35_0P8B as D
     from qwen35_b200.model import Decoder
@@ -150,7 +150,7 @@ def prefill_sweep(weights_gpu, dev, lengths):
 
 
 def tree_verify_bench(dev, n_nodes=33, ctx=4096, iters=5):
-    """27B-class dims, Q4_K weights generated directly as random super-blocks (dequantised
+    """Tree-verify configuration: 27B-class dims, Q4_K weights generated directly as random super-blocks (dequantised
     sigma ~0.02), a 4096-token context of random cache contents, one 33-node tree (seeded random parents, depth <= 8):
     milliseconds per verify + accept walk + commit, timed with CUDA events."""
     from qwen35_b200.tree_verify import QWEN35_27B as T, TreeTarget, make_random_tree_weights, random_tree
@@ -185,13 +185,13 @@ def tree_verify_bench(dev, n_nodes=33, ctx=4096, iters=5):
     st_bytes = T.n_dn * n_nodes * T.dn_v_heads * T.dn_dim * T.dn_dim * 2
     alg = w_bytes + kv_bytes + st_bytes
     flops = 2 * (24_352_522_240 + 1_271_398_400) * n_nodes
-    return {"workload": "BASELINE configs[4]: 27B-class dims (64 layers, hidden 5120), Q4_K weights, %d-token context, %d-node tree" % (ctx, n_nodes),
+    return {"workload": "tree verify: 27B-class dims (64 layers, hidden 5120), Q4_K weights, %d-token context, %d-node tree" % (ctx, n_nodes),
             "ms_per_verify_commit": ms, "accepted": acc, "launches_per_pass": int(launches), "algorithmic_bytes": alg, "hbm_gbs": alg / (ms * 1e-3) / 1e9,
             "roofline_frac": alg / (ms * 1e-3) / 1e9 / measured_peak()[0], "tflops": flops / (ms * 1e-3) / 1e12}
 
 
 def batched_decode_bench(weights_gpu, dev, rank, n_seq, ctx, n_steps, kernel_table=False):
-    """`n_seq` independent sequences per GPU, `ctx`-token contexts prefilled by the library's own
+    """Batched-decode configuration: `n_seq` independent sequences per GPU, `ctx`-token contexts prefilled by the library's own
     prefill, `n_steps` greedy steps.  Returns (tok/s on this rank, ms per step, algorithmic bytes per step)."""
     from qwen35_b200.config import QWEN35_0P8B as D
     from qwen35_b200.model import BatchedDecoder
@@ -262,7 +262,7 @@ def cpu_baseline(weights_cpu, ids, n_decode=16, use_hf=False):
 
 
 def tree_cpu_baseline(n_nodes=8, layers=2, vocab=4096):
-    """CPU side of BASELINE configs[4]: the path-sequential oracle at the 27B widths on a reduced model (`layers` of
+    """CPU side of the tree-verify configuration: the path-sequential oracle at the 27B widths on a reduced model (`layers` of
     64 layers, one DeltaNet + one attention; `vocab` of 248 320 LM-head rows; an 8-node chain on an empty context),
     timed per node-layer and extrapolated to 33 nodes x 64 layers.  Reported, not a target."""
     import dataclasses
@@ -422,7 +422,7 @@ def run_ours(args):
         job = reduce_counters(tokens=args.batched * GEN, elapsed_ms=b_ms * GEN, algorithmic_bytes=b_bytes * GEN, device=dev)
         b_ms = job.elapsed_ms / GEN                         # slowest rank's time per step
         b_tok_s = job.tokens_per_s / world                  # per-GPU rate of the whole job
-        batched = {"workload": "BASELINE configs[3]: %d sequences per GPU, %d-token contexts, %d greedy steps, no collectives" % (args.batched, args.batched_ctx, GEN),
+        batched = {"workload": "batched decode: %d sequences per GPU, %d-token contexts, %d greedy steps, no collectives" % (args.batched, args.batched_ctx, GEN),
                    "value": world * b_tok_s, "unit": "tok/s", "per_gpu_tok_s": b_tok_s, "ms_per_step": b_ms,
                    "algorithmic_bytes_per_step": b_bytes, "hbm_gbs": b_bytes / (b_ms * 1e-3) / 1e9,
                    "roofline_frac": b_bytes / (b_ms * 1e-3) / 1e9 / measured_peak()[0]}

@@ -434,7 +434,7 @@ KV_PAGE = 64
 
 
 class BatchedDecoder:
-    """`batch` independent sequences decoded together on one GPU (BASELINE configuration "64 sequences per GPU").
+    """`batch` independent sequences decoded together on one GPU (the benchmark configuration "64 sequences per GPU").
     Each sequence owns its DeltaNet state, conv window and KV pages; weights are shared.  Prefill a sequence with
     `prefill(seq, ids)` (runs the bs=1 batched-prefill kernels into that sequence's slots), then `step()` advances
     every sequence by one greedy token."""

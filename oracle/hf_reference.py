@@ -1,6 +1,6 @@
 """The reference's own CPU ground truth: HuggingFace `transformers` eager Qwen3.5 with the
 pure-torch DeltaNet functions (the "PyTorch HF" arm of models/qwen35_0p8b/final_bench.py:241-304).
-TEST / BASELINE INFRASTRUCTURE ONLY -- never imported by the product package.
+TEST / CPU-BASELINE INFRASTRUCTURE ONLY -- never imported by the product package.
 
 `transformers` (5.5.0, models/qwen3_5) is a third-party dependency of the reference that is
 installed in this image; nothing is copied from it.  Used by tests/golden/make_golden.py to
