@@ -84,6 +84,12 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.p.kill()
             out, _ = self.p.communicate()
+        if not out.strip():            # nothing delivered in time: one query now, the GPU has just finished the region
+            try:
+                out = subprocess.run(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-i", str(self.idx)],
+                                     capture_output=True, text=True, timeout=20).stdout
+            except (OSError, subprocess.TimeoutExpired):
+                out = ""
         sm, mx, reasons = [], [], set()
         for line in out.splitlines():
             f = [x.strip() for x in line.split(",")]
@@ -367,11 +373,13 @@ def run_ours(args):
             torch.distributed.barrier()
         torch.cuda.synchronize(dev)
 
+    # the sampler starts before the warm-up steps (same kernels, same load): nvidia-smi needs up to a second to deliver
+    # its first line, longer than a short timed region
+    sampler = ClockSampler(local_rank)
+    sampler.start()
     for _ in range(max(args.warmup, 3)):
         step_device()
     barrier()
-    sampler = ClockSampler(local_rank)
-    sampler.start()
     launches0 = lib.qwen35_b200_launch_count()
     k_ev = []
     barrier()
