@@ -232,7 +232,8 @@ typedef struct {
 
 /* Weights of one layer.  Q4_K matrices are row-major arrays of 144-byte super-blocks (256 weights each), rows of the
  * fused matrices concatenated (a GGUF loader concatenates the tensors' bytes: attn_q|attn_k|attn_v, attn_qkv|attn_gate,
- * ffn_gate|ffn_up; tensor names src/gguf_target_loader.cpp:7-39).  Norm and SSM vectors are f32 as in GGUF. */
+ * ffn_gate|ffn_up; tensor names src/gguf_target_loader.cpp:7-39).  Norm and SSM vectors are f32 as in GGUF.  A matrix
+ * whose tensors are stored in another type is handed over dequantised to plain bf16 and flagged in dense_mask. */
 typedef struct {
     const void* attn_norm;   /* f32 [hidden], applied as a plain multiply */
     const void* post_norm;   /* f32 [hidden] */
@@ -247,7 +248,8 @@ typedef struct {
     const void* ssm_a;       /* DN: f32 [v_heads], -exp(A_log) */
     const void* dt_bias;     /* DN: f32 [v_heads] */
     const void* ssm_norm;    /* DN: f32 [128] */
-    const void* reserved[3];
+    unsigned long long dense_mask;   /* bit 0 w_in, 1 w_out, 2 w_gate_up, 3 w_down: that matrix is plain bf16 [rows][cols], not Q4_K */
+    const void* reserved[2];
 } Qwen35TreeLayer;
 
 typedef struct {
@@ -271,6 +273,7 @@ typedef struct {
     int dbg_num_layers;              /* > 0: stop after this many layers (the head still runs) */
     void* scratch; size_t scratch_bytes;   /* caller-owned, >= qwen35_b200_tree_scratch_bytes() */
     const void* dbg_teacher;         /* optional bf16 [n_layers][n_nodes][hidden]: layer l > 0 reads row block l as its input */
+    unsigned int dense_mask;         /* bit 0: token_embd is plain bf16 [vocab][hidden]; bit 1: output_w is */
 } Qwen35TreeVerifyArgs;
 
 size_t qwen35_b200_tree_scratch_bytes(const Qwen35TreeDims* dims, int n_nodes, int max_ctx);

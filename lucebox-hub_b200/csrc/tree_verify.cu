@@ -593,10 +593,20 @@ static bool tv_dims_ok(const TvDims& D) {
            D.rot_dim % 2 == 0 && D.rot_dim <= TV_HD && D.dn_v_heads % D.dn_k_heads == 0 && D.n_layers > 0 && D.fa_period > 0 && D.vocab > 0;
 }
 
-// C[M, out_rows] = epi(X[M, in] . dequant(W[out_rows, in])^T) in one launch.  epi 2: W = [gate rows ; up rows], out = ffn
-static int q4k_linear(const bf16* X, int lda, const uint8_t* W, int out_rows, int in_cols, bf16* C, int ldc, const bf16* R, int ldr,
+// C[M, out_rows] = epi(X[M, in] . W[out_rows, in]^T) in one launch.  epi 2: W = [gate rows ; up rows], out = ffn.
+// W is Q4_K super-blocks (dequantised in the kernel) or, when `dense`, plain bf16 [rows][in] (what a loader makes of a
+// tensor stored in another quantisation type).
+static int q4k_linear(const bf16* X, int lda, const void* W, bool dense, int out_rows, int in_cols, bf16* C, int ldc, const bf16* R, int ldr,
                       int M, int epi, cudaStream_t stream) {
-    return gemm_q4k(X, lda, W, epi == 2 ? 2 * out_rows : out_rows, C, ldc, R, ldr, M, out_rows, in_cols, epi, out_rows, stream);
+    const int w_rows = epi == 2 ? 2 * out_rows : out_rows;
+    if (dense) return gemm_bf16(X, lda, (const bf16*)W, w_rows, C, ldc, R, ldr, M, out_rows, in_cols, epi, out_rows, stream);
+    return gemm_q4k(X, lda, (const uint8_t*)W, w_rows, C, ldc, R, ldr, M, out_rows, in_cols, epi, out_rows, stream);
+}
+
+// embedding rows from a dense bf16 table
+__global__ void __launch_bounds__(256) tv_embed_dense_kernel(const bf16* __restrict__ embd, const int* __restrict__ tokens, int hidden, bf16* __restrict__ out) {
+    const bf16* src = embd + (size_t)tokens[blockIdx.x] * hidden;
+    for (int i = threadIdx.x; i < hidden; i += 256) out[(size_t)blockIdx.x * hidden + i] = src[i];
 }
 
 }  // namespace q35
@@ -670,7 +680,8 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
     if (in->max_nodes < n) { set_error("tree_verify: max_nodes %d < n_nodes %d", in->max_nodes, n); return QWEN35_ERR_BAD_ARG; }
 
     tv_tree_prep_kernel<<<1, 32, 0, stream>>>(in->parents, n, s.depth, s.anc);
-    tv_embed_q4k_kernel<<<dim3(n, D.hidden / 256), 32, 0, stream>>>((const uint8_t*)in->token_embd, in->node_tokens, D.hidden, s.hidden);
+    if (in->dense_mask & 1u) tv_embed_dense_kernel<<<n, 256, 0, stream>>>((const bf16*)in->token_embd, in->node_tokens, D.hidden, s.hidden);
+    else tv_embed_q4k_kernel<<<dim3(n, D.hidden / 256), 32, 0, stream>>>((const uint8_t*)in->token_embd, in->node_tokens, D.hidden, s.hidden);
     g_launches.fetch_add(2);
     const int n_layers = in->dbg_num_layers > 0 && in->dbg_num_layers < D.n_layers ? in->dbg_num_layers : D.n_layers;
     int i_fa = 0, i_dn = 0;
@@ -683,7 +694,7 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
         g_launches.fetch_add(1);
         int att_w;
         if (is_fa) {
-            Q35_TRYT(q4k_linear(s.normed, D.hidden, (const uint8_t*)W.w_in, fa_in, D.hidden, s.proj, fa_in, nullptr, 0, n, 0, stream));
+            Q35_TRYT(q4k_linear(s.normed, D.hidden, W.w_in, (W.dense_mask & 1u) != 0, fa_in, D.hidden, s.proj, fa_in, nullptr, 0, n, 0, stream));
             bf16* kc = (bf16*)in->k_cache + (size_t)i_fa * kv_layer;
             bf16* vc = (bf16*)in->v_cache + (size_t)i_fa * kv_layer;
             tv_fa_prep_kernel<<<dim3(n, D.q_heads + 2 * D.kv_heads), 128, 0, stream>>>(s.proj, fa_in, (const float*)W.q_norm, (const float*)W.k_norm, s.depth, D,
@@ -696,7 +707,7 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
             att_w = D.q_heads * TV_HD;
             ++i_fa;
         } else {
-            Q35_TRYT(q4k_linear(s.normed, D.hidden, (const uint8_t*)W.w_in, dn_in, D.hidden, s.proj, dn_in, nullptr, 0, n, 0, stream));
+            Q35_TRYT(q4k_linear(s.normed, D.hidden, W.w_in, (W.dense_mask & 1u) != 0, dn_in, D.hidden, s.proj, dn_in, nullptr, 0, n, 0, stream));
             Q35_TRYT(gemm_bf16(s.normed, D.hidden, (const bf16*)W.w_ba, 2 * D.dn_v_heads, s.ba, 2 * D.dn_v_heads, nullptr, 0, n, 2 * D.dn_v_heads, D.hidden, 0, 0, stream));
             float* cstate = (float*)in->conv_state + (size_t)i_dn * 3 * conv_ch;
             float* nconv = (float*)in->node_conv + (size_t)i_dn * nconv_layer;
@@ -710,16 +721,16 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
             att_w = D.dn_v_heads * TV_DN;
             ++i_dn;
         }
-        Q35_TRYT(q4k_linear(s.attn, att_w, (const uint8_t*)W.w_out, D.hidden, att_w, s.resid, D.hidden, s.hidden, D.hidden, n, 1, stream));
+        Q35_TRYT(q4k_linear(s.attn, att_w, W.w_out, (W.dense_mask & 2u) != 0, D.hidden, att_w, s.resid, D.hidden, s.hidden, D.hidden, n, 1, stream));
         tv_rmsnorm_kernel<<<n, 256, 0, stream>>>(s.resid, (const float*)W.post_norm, s.normed, D.hidden, D.eps);
         g_launches.fetch_add(1);
-        Q35_TRYT(q4k_linear(s.normed, D.hidden, (const uint8_t*)W.w_gate_up, D.ffn, D.hidden, s.mlp, D.ffn, nullptr, 0, n, 2, stream));
-        Q35_TRYT(q4k_linear(s.mlp, D.ffn, (const uint8_t*)W.w_down, D.hidden, D.ffn, s.hidden, D.hidden, s.resid, D.hidden, n, 1, stream));
+        Q35_TRYT(q4k_linear(s.normed, D.hidden, W.w_gate_up, (W.dense_mask & 4u) != 0, D.ffn, D.hidden, s.mlp, D.ffn, nullptr, 0, n, 2, stream));
+        Q35_TRYT(q4k_linear(s.mlp, D.ffn, W.w_down, (W.dense_mask & 8u) != 0, D.hidden, D.ffn, s.hidden, D.hidden, s.resid, D.hidden, n, 1, stream));
         if (in->dbg_hidden)
             Q35_CUDA_OK(cudaMemcpyAsync((bf16*)in->dbg_hidden + (size_t)il * n * D.hidden, s.hidden, (size_t)n * D.hidden * 2, cudaMemcpyDeviceToDevice, stream));
     }
     tv_rmsnorm_kernel<<<n, 256, 0, stream>>>(s.hidden, (const float*)in->output_norm, s.normed, D.hidden, D.eps);
-    Q35_TRYT(q4k_linear(s.normed, D.hidden, (const uint8_t*)in->output_w, D.vocab, D.hidden, s.logits, D.vocab, nullptr, 0, n, 0, stream));
+    Q35_TRYT(q4k_linear(s.normed, D.hidden, in->output_w, (in->dense_mask & 2u) != 0, D.vocab, D.hidden, s.logits, D.vocab, nullptr, 0, n, 0, stream));
     tv_argmax_kernel<<<n, 1024, 0, stream>>>(s.logits, D.vocab, in->node_argmax);
     g_launches.fetch_add(2);
     if (in->logits_out) Q35_CUDA_OK(cudaMemcpyAsync(in->logits_out, s.logits, (size_t)n * D.vocab * 2, cudaMemcpyDeviceToDevice, stream));

@@ -66,7 +66,7 @@ class TreeDimsC(C.Structure):
 
 class TreeLayerC(C.Structure):
     _fields_ = [(k, C.c_void_p) for k in ("attn_norm", "post_norm", "w_in", "w_ba", "w_out", "w_gate_up", "w_down", "q_norm", "k_norm", "conv_w",
-                                           "ssm_a", "dt_bias", "ssm_norm", "r0", "r1", "r2")]
+                                           "ssm_a", "dt_bias", "ssm_norm")] + [("dense_mask", C.c_ulonglong), ("r1", C.c_void_p), ("r2", C.c_void_p)]
 
 
 class TreeVerifyArgs(C.Structure):
@@ -75,7 +75,7 @@ class TreeVerifyArgs(C.Structure):
         ("n_nodes", C.c_int), ("max_nodes", C.c_int), ("node_tokens", C.c_void_p), ("parents", C.c_void_p), ("past", C.c_int), ("max_ctx", C.c_int),
         ("k_cache", C.c_void_p), ("v_cache", C.c_void_p), ("ssm_state", C.c_void_p), ("conv_state", C.c_void_p), ("node_states", C.c_void_p),
         ("node_conv", C.c_void_p), ("node_argmax", C.c_void_p), ("logits_out", C.c_void_p), ("dbg_hidden", C.c_void_p), ("dbg_num_layers", C.c_int),
-        ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t), ("dbg_teacher", C.c_void_p),
+        ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t), ("dbg_teacher", C.c_void_p), ("dense_mask", C.c_uint),
     ]
 
 

@@ -3,9 +3,11 @@
 `qwen35` hyper-parameters, and assembles the weight layout of `Qwen35TreeLayer`: matrices that the pass consumes fused
 (q|k|v, qkv|z, gate|up) are row concatenations of the tensors' raw super-block bytes, so nothing is re-quantised.
 
-Supported tensor types: Q4_K for the matrices (they stay quantised: the GEMM dequantises in the kernel), F32 / F16 /
-BF16 for vectors and the small beta / alpha projections.  A matrix of another type (published mixed files carry Q5_K,
-Q6_K, Q8_0 and IQ4_XS tensors) is refused by name and type rather than silently converted."""
+Matrices whose tensors are all Q4_K stay quantised (the GEMM dequantises in the kernel).  A (fused) matrix with a tensor
+of another type -- published mixed files carry Q5_K, Q6_K, Q8_0 and IQ4_XS tensors -- is dequantised on the host with
+gguf-py's reference routines and handed over as plain bf16 (`allow_dense=True`, the default; 3.5 x the bytes of Q4_K
+for that matrix), or refused by name and type (`allow_dense=False`).  Vectors and the small beta / alpha projections
+are F32 / F16 / BF16."""
 import numpy as np
 import torch
 
@@ -41,7 +43,7 @@ def read_dims(reader) -> TreeDims:
                     rope_theta=float(k("rope.freq_base", 1.0e7)), rms_eps=float(k("attention.layer_norm_rms_epsilon", 1.0e-6)))
 
 
-def load_gguf_target(path: str, device="cuda"):
+def load_gguf_target(path: str, device="cuda", allow_dense: bool = True):
     """Returns (TreeDims, weights dict for qwen35_b200.tree_verify.TreeTarget)."""
     import dataclasses
 
@@ -57,13 +59,35 @@ def load_gguf_target(path: str, device="cuda"):
             raise KeyError(f"tensor {name} missing from {path}")
         return tensors[name]
 
-    def q4k(name, rows, cols):
-        t = need(name)
-        if t.tensor_type != T.Q4_K:
-            raise TypeError(f"{name}: type {t.tensor_type.name} is not supported for a weight matrix (Q4_K only)")
-        if [int(x) for x in t.shape] != [cols, rows]:
-            raise ValueError(f"{name}: shape {list(t.shape)}, expected [{cols}, {rows}]")
+    def q4k_blocks(t, rows, cols):
         return torch.from_numpy(np.array(t.data, dtype=np.uint8).reshape(rows, cols // 256, 144))
+
+    def dense(t, rows, cols):
+        from gguf.quants import dequantize
+        if t.tensor_type == T.F32:
+            a = np.array(t.data, dtype=np.float32)
+        elif t.tensor_type == T.F16:
+            a = np.array(t.data, dtype=np.float16).astype(np.float32)
+        elif t.tensor_type == T.BF16:
+            return torch.from_numpy(np.ascontiguousarray(t.data).view(np.int16).copy()).view(torch.bfloat16).reshape(rows, cols)
+        else:
+            a = dequantize(np.array(t.data), t.tensor_type).astype(np.float32)
+        return torch.from_numpy(a.reshape(rows, cols)).bfloat16()
+
+    def matrix(parts, cols):
+        """parts = [(tensor name, rows)]: the row-wise fusion of those tensors, Q4_K blocks if every part is Q4_K."""
+        ts = []
+        for name, rows in parts:
+            t = need(name)
+            if [int(x) for x in t.shape] != [cols, rows]:
+                raise ValueError(f"{name}: shape {list(t.shape)}, expected [{cols}, {rows}]")
+            ts.append((t, rows))
+        if all(t.tensor_type == T.Q4_K for t, _ in ts) and cols % 256 == 0:
+            return torch.cat([q4k_blocks(t, rows, cols) for t, rows in ts], 0)
+        if not allow_dense:
+            bad = next(t for t, _ in ts if t.tensor_type != T.Q4_K)
+            raise TypeError(f"{bad.name}: type {bad.tensor_type.name} is not supported for a weight matrix (Q4_K only)")
+        return torch.cat([dense(t, rows, cols) for t, rows in ts], 0)
 
     def vec(name, shape):
         t = need(name)
@@ -86,27 +110,27 @@ def load_gguf_target(path: str, device="cuda"):
     for il in range(D.n_layers):
         p = f"blk.{il}."
         L = {"attn_norm": vec(p + "attn_norm.weight", (H,)), "post_norm": vec(p + "post_attention_norm.weight", (H,)),
-             "w_gate_up": torch.cat([q4k(p + "ffn_gate.weight", D.ffn, H), q4k(p + "ffn_up.weight", D.ffn, H)], 0),
-             "w_down": q4k(p + "ffn_down.weight", H, D.ffn)}
+             "w_gate_up": matrix([(p + "ffn_gate.weight", D.ffn), (p + "ffn_up.weight", D.ffn)], H),
+             "w_down": matrix([(p + "ffn_down.weight", H)], D.ffn)}
         if D.is_fa(il):
             qd, kvd = D.q_heads * D.head_dim, D.kv_heads * D.head_dim
-            L["w_in"] = torch.cat([q4k(p + "attn_q.weight", 2 * qd, H), q4k(p + "attn_k.weight", kvd, H), q4k(p + "attn_v.weight", kvd, H)], 0)
-            L["w_out"] = q4k(p + "attn_output.weight", H, qd)
+            L["w_in"] = matrix([(p + "attn_q.weight", 2 * qd), (p + "attn_k.weight", kvd), (p + "attn_v.weight", kvd)], H)
+            L["w_out"] = matrix([(p + "attn_output.weight", H)], qd)
             L["q_norm"] = vec(p + "attn_q_norm.weight", (D.head_dim,))
             L["k_norm"] = vec(p + "attn_k_norm.weight", (D.head_dim,))
         else:
             inner = D.dn_v_heads * D.dn_dim
-            L["w_in"] = torch.cat([q4k(p + "attn_qkv.weight", D.conv_ch, H), q4k(p + "attn_gate.weight", inner, H)], 0)
-            L["w_out"] = q4k(p + "ssm_out.weight", H, inner)
+            L["w_in"] = matrix([(p + "attn_qkv.weight", D.conv_ch), (p + "attn_gate.weight", inner)], H)
+            L["w_out"] = matrix([(p + "ssm_out.weight", H)], inner)
             L["w_ba"] = torch.cat([vec(p + "ssm_beta.weight", (D.dn_v_heads, H)), vec(p + "ssm_alpha.weight", (D.dn_v_heads, H))], 0).bfloat16()
             L["conv_w"] = vec(p + "ssm_conv1d.weight", (D.conv_ch, 4))
             L["ssm_a"] = vec(p + "ssm_a", (D.dn_v_heads,))
             L["dt_bias"] = vec(p + "ssm_dt.bias", (D.dn_v_heads,))
             L["ssm_norm"] = vec(p + "ssm_norm.weight", (D.dn_dim,))
         layers.append({k: v.to(device) for k, v in L.items()})
-    w = {"layers": layers, "token_embd": q4k("token_embd.weight", vocab, H).to(device),
+    w = {"layers": layers, "token_embd": matrix([("token_embd.weight", vocab)], H).to(device),
          "output_norm": vec("output_norm.weight", (H,)).to(device),
-         "output_w": q4k("output.weight" if "output.weight" in tensors else "token_embd.weight", vocab, H).to(device)}
+         "output_w": matrix([("output.weight" if "output.weight" in tensors else "token_embd.weight", vocab)], H).to(device)}
     return D, w
 
 

@@ -135,10 +135,18 @@ class TreeTarget:
         self._dims_c = _capi.TreeDimsC(D.n_layers, D.hidden, D.ffn, D.vocab, D.q_heads, D.kv_heads, D.head_dim, D.dn_k_heads, D.dn_v_heads, D.dn_dim,
                                        D.rot_dim, D.fa_period, D.rope_theta, D.rms_eps)
         self._layers_c = (_capi.TreeLayerC * D.n_layers)()
+        # a matrix given as bf16 [rows, cols] instead of Q4_K super-blocks (uint8 [rows, cols/256, 144]) is flagged dense
+        mat_bit = {"w_in": 1, "w_out": 2, "w_gate_up": 4, "w_down": 8}
         for il, L in enumerate(weights["layers"]):
+            mask = 0
             for k, v in L.items():
                 assert v.is_cuda and v.is_contiguous(), k
                 setattr(self._layers_c[il], k, v.data_ptr())
+                if k in mat_bit:
+                    assert v.dtype in (torch.uint8, torch.bfloat16), k
+                    mask |= mat_bit[k] if v.dtype == torch.bfloat16 else 0
+            self._layers_c[il].dense_mask = mask
+        self._dense_mask = (1 if weights["token_embd"].dtype == torch.bfloat16 else 0) | (2 if weights["output_w"].dtype == torch.bfloat16 else 0)
         dev = self.device
         self.k_cache = torch.zeros(max(D.n_fa, 1), D.kv_heads, self.max_ctx, D.head_dim, dtype=torch.bfloat16, device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
@@ -169,6 +177,7 @@ class TreeTarget:
         a.node_states = self.node_states.data_ptr(); a.node_conv = self.node_conv.data_ptr()
         a.node_argmax = self.node_argmax.data_ptr()
         a.scratch = self._scratch.data_ptr(); a.scratch_bytes = self._scratch.numel()
+        a.dense_mask = self._dense_mask
         for k, v in kw.items():
             setattr(a, k, _capi.ptr(v) if torch.is_tensor(v) else v)
         return a

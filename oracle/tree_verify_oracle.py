@@ -106,7 +106,7 @@ class TreeOracle:
             self.layers.append(M)
         self.embd_blocks = weights["token_embd"]
         self.output_norm = weights["output_norm"].float()
-        self.output_w = mat(weights["output_w"])
+        self.output_w = mat(weights["output_w"]) if weights["output_w"].dtype == torch.uint8 else weights["output_w"].float()
         # committed context
         self.k = [torch.zeros(D.kv_heads, 0, D.head_dim) for _ in range(D.n_fa)]
         self.v = [torch.zeros(D.kv_heads, 0, D.head_dim) for _ in range(D.n_fa)]
@@ -135,7 +135,10 @@ class TreeOracle:
         (logits bf16-valued f32 [vocab], new ctx, per-layer hidden list)."""
         D = self.D
         nb = D.hidden // 256
-        x = rb(torch.from_numpy(q4k_dequant(self.embd_blocks[token].numpy().reshape(nb, 144))).reshape(D.hidden))
+        if self.embd_blocks.dtype == torch.uint8:
+            x = rb(torch.from_numpy(q4k_dequant(self.embd_blocks[token].numpy().reshape(nb, 144))).reshape(D.hidden))
+        else:                                   # a dense bf16 table
+            x = self.embd_blocks[token].float()
         new = {"k": [], "v": [], "ssm": [], "conv": []}
         hid = []
         i_fa = i_dn = 0

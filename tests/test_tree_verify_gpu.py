@@ -244,3 +244,51 @@ def test_tree_verify_on_a_best_first_tree():
         for j in range(len(i_dn)):
             ref_s = ctxs[t]["ssm"][j]
             assert float((tt.node_states[j, t].float().cpu() - ref_s).norm() / ref_s.norm().clamp_min(1e-6)) <= STATE_REL_TOL
+
+
+def test_tree_verify_with_dense_bf16_matrices():
+    """Matrices a loader dequantised to bf16 (tensors stored as Q8_0, Q6_K, ... in published files) run through the
+    bf16 GEMM in the same pass as Q4_K ones: attention input projection, down projection, LM head and embedding dense."""
+    from oracle.tree_verify_oracle import TreeOracle, q4k_dequant
+    from qwen35_b200.tree_verify import TreeTarget, make_random_tree_weights, random_tree
+    D = small_dims()
+    w = make_random_tree_weights(D, 31)
+
+    def densify(blocks):
+        r, nb, _ = blocks.shape
+        return torch.from_numpy(q4k_dequant(blocks.numpy().reshape(-1, 144))).reshape(r, nb * 256).bfloat16()
+
+    for L in w["layers"]:
+        L["w_down"] = densify(L["w_down"])
+    w["layers"][3]["w_in"] = densify(w["layers"][3]["w_in"])
+    w["output_w"] = densify(w["output_w"]); w["token_embd"] = densify(w["token_embd"])
+    orc = TreeOracle(D, w, 128)
+    rng = np.random.default_rng(5)
+    orc.feed(rng.integers(0, D.vocab, 20))
+    wg = {"layers": [{k: v.cuda() for k, v in L.items()} for L in w["layers"]],
+          "token_embd": w["token_embd"].cuda(), "output_norm": w["output_norm"].cuda(), "output_w": w["output_w"].cuda()}
+    tt = TreeTarget(D, wg, max_ctx=128)
+    for i in range(D.n_fa):
+        tt.k_cache[i, :, :20] = orc.k[i].bfloat16().cuda(); tt.v_cache[i, :, :20] = orc.v[i].bfloat16().cuda()
+    for i in range(D.n_dn):
+        tt.ssm_state[i] = orc.ssm[i].cuda(); tt.conv_state[i] = orc.conv[i].cuda()
+    tt.past = 20
+    parents = random_tree(10, 4, 8)
+    tokens = rng.integers(0, D.vocab, 10)
+    ref_logits, _, hids = orc.verify(tokens, parents)
+    teacher = torch.zeros(D.n_layers, 10, D.hidden, dtype=torch.bfloat16)
+    for t in range(10):
+        for il in range(1, D.n_layers):
+            teacher[il, t] = hids[t][il - 1].bfloat16()
+    dbg = torch.zeros(D.n_layers, 10, D.hidden, dtype=torch.bfloat16, device="cuda")
+    tt.verify(torch.tensor(tokens, dtype=torch.int32), torch.tensor(parents, dtype=torch.int32), dbg_hidden=dbg, dbg_teacher=teacher.cuda())
+    tt.check_status()
+    got = dbg.float().cpu()
+    for t in range(10):
+        for il in range(D.n_layers):
+            assert float((got[il, t] - hids[t][il]).abs().max()) <= LAYER_ABS_TOL, (t, il)
+    lg = torch.zeros(10, D.vocab, dtype=torch.bfloat16, device="cuda")
+    tt.verify(torch.tensor(tokens, dtype=torch.int32), torch.tensor(parents, dtype=torch.int32), logits_out=lg)
+    tt.check_status()
+    for t in range(10):
+        assert float((lg[t].float().cpu() - ref_logits[t]).abs().max()) <= LOGIT_TOL
