@@ -160,6 +160,53 @@ __device__ __forceinline__ void epilogue_store8(const GemmParams& p, int row, in
     }
 }
 
+// Second half of the split-K epilogue: every CTA of the cluster has parked its f32 tile [column][row] at the same
+// shared-memory offset; CTA `rank` finishes columns [rank * BN_OUT / S, +BN_OUT / S) for `rows` rows.  A work item is one
+// row x 8 adjacent columns: all peers' values are requested before the first is used (one remote round trip, not S), then
+// summed in peer order, so the result does not depend on timing.  `t` is the calling thread's index among `nt` workers.
+template <int EPI>
+__device__ __forceinline__ void cluster_reduce_store(const GemmParams& p, uint32_t park_local, int S, int rows, int m0, int n0, int t, int nt) {
+    constexpr int BN_OUT = (EPI == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
+    const uint32_t rank = cluster_ctarank();
+    const int slice = BN_OUT / S;                       // a multiple of 8
+    for (int item = t; item < rows * (slice / 8); item += nt) {
+        const int r = item % rows, cg = item / rows;
+        const int col = (int)rank * slice + cg * 8;     // first of 8 output columns within the tile
+        float g[8], u[8], v[GEMM_MAX_SPLIT][8];
+#pragma unroll
+        for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
+            if (peer < S) {
+                const uint32_t base = map_to_cta(park_local, (uint32_t)peer);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[peer][e] = ld_dsmem(base + (uint32_t)(((col + e) * GEMM_BM + r) * 4));
+            }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) { g[e] = 0.f; u[e] = 0.f; }
+#pragma unroll
+        for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
+            if (peer < S) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) g[e] += v[peer][e];
+            }
+        if (EPI == EPI_SILU_MUL) {
+#pragma unroll
+            for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
+                if (peer < S) {
+                    const uint32_t base = map_to_cta(park_local, (uint32_t)peer);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) v[peer][e] = ld_dsmem(base + (uint32_t)(((64 + col + e) * GEMM_BM + r) * 4));
+                }
+#pragma unroll
+            for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
+                if (peer < S) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) u[e] += v[peer][e];
+                }
+        }
+        epilogue_store8<EPI>(p, m0 + r, n0 + col, g, u);
+    }
+}
+
 // SPLIT: gridDim.z = cluster size S along K (1, 2, 4 or 8); the cluster shares one output tile
 template <int EPI, int STAGES, bool SPLIT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
@@ -281,51 +328,8 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
         // every thread of every CTA of the cluster passes both barriers, whatever happened above
         __syncwarp();
         cluster_sync_all();
-        if (warp >= 2 && !*s_abort) {
-            const uint32_t rank = cluster_ctarank();
-            const int slice = BN_OUT / S;                       // output columns this CTA finishes (a multiple of 8)
-            const int rows = min(GEMM_BM, p.M - m0);
-            const uint32_t park_local = tiles;
-            for (int item = (int)threadIdx.x - 64; item < rows * (slice / 8); item += GEMM_THREADS - 64) {
-                const int r = item % rows, cg = item / rows;
-                const int col = (int)rank * slice + cg * 8;     // first of 8 output columns within the tile
-                float g[8], u[8];
-                // all peers' values are requested before the first is used (one remote round trip, not S), then
-                // summed in peer order: the result does not depend on timing
-                float v[GEMM_MAX_SPLIT][8];
-#pragma unroll
-                for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
-                    if (peer < S) {
-                        const uint32_t base = map_to_cta(park_local, (uint32_t)peer);
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) v[peer][e] = ld_dsmem(base + (uint32_t)(((col + e) * GEMM_BM + r) * 4));
-                    }
-#pragma unroll
-                for (int e = 0; e < 8; ++e) { g[e] = 0.f; u[e] = 0.f; }
-#pragma unroll
-                for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
-                    if (peer < S) {
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) g[e] += v[peer][e];
-                    }
-                if (EPI == EPI_SILU_MUL) {
-#pragma unroll
-                    for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
-                        if (peer < S) {
-                            const uint32_t base = map_to_cta(park_local, (uint32_t)peer);
-#pragma unroll
-                            for (int e = 0; e < 8; ++e) v[peer][e] = ld_dsmem(base + (uint32_t)(((64 + col + e) * GEMM_BM + r) * 4));
-                        }
-#pragma unroll
-                    for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
-                        if (peer < S) {
-#pragma unroll
-                            for (int e = 0; e < 8; ++e) u[e] += v[peer][e];
-                        }
-                }
-                epilogue_store8<EPI>(p, m0 + r, n0 + col, g, u);
-            }
-        }
+        if (warp >= 2 && !*s_abort)
+            cluster_reduce_store<EPI>(p, tiles, S, min(GEMM_BM, p.M - m0), m0, n0, (int)threadIdx.x - 64, GEMM_THREADS - 64);
         __syncwarp();
         cluster_sync_all();                                     // no CTA leaves while a peer may still read its tile
     }
@@ -549,48 +553,7 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
     }
     __syncwarp();
     cluster_sync_all();
-    if (warp >= 2 && !*s_abort) {
-        const uint32_t rank = cluster_ctarank();
-        const int slice = BN_OUT / S;
-        const int rows = min(64, p.M);
-        const uint32_t park_local = tiles;
-        for (int item = (int)threadIdx.x - 64; item < rows * (slice / 8); item += Q4K_THREADS - 64) {
-            const int rr = item % rows, cg = item / rows;
-            const int col = (int)rank * slice + cg * 8;
-            float g[8], u[8], v[GEMM_MAX_SPLIT][8];
-#pragma unroll
-            for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
-                if (peer < S) {
-                    const uint32_t base = map_to_cta(park_local, (uint32_t)peer);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) v[peer][e] = ld_dsmem(base + (uint32_t)(((col + e) * GEMM_BM + rr) * 4));
-                }
-#pragma unroll
-            for (int e = 0; e < 8; ++e) { g[e] = 0.f; u[e] = 0.f; }
-#pragma unroll
-            for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
-                if (peer < S) {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) g[e] += v[peer][e];
-                }
-            if (EPI == EPI_SILU_MUL) {
-#pragma unroll
-                for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
-                    if (peer < S) {
-                        const uint32_t base = map_to_cta(park_local, (uint32_t)peer);
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) v[peer][e] = ld_dsmem(base + (uint32_t)(((64 + col + e) * GEMM_BM + rr) * 4));
-                    }
-#pragma unroll
-                for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
-                    if (peer < S) {
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) u[e] += v[peer][e];
-                    }
-            }
-            epilogue_store8<EPI>(p, rr, n0 + col, g, u);
-        }
-    }
+    if (warp >= 2 && !*s_abort) cluster_reduce_store<EPI>(p, tiles, S, min(64, p.M), 0, n0, (int)threadIdx.x - 64, Q4K_THREADS - 64);
     __syncwarp();
     cluster_sync_all();
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");

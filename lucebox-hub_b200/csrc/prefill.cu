@@ -72,12 +72,9 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
     if (!attr_done) {
         Q35_CUDA_OK(cudaFuncSetAttribute(pf_dn_chunk_local_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CHUNK_LOCAL_SMEM));
         Q35_CUDA_OK(cudaFuncSetAttribute(pf_dn_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CHUNK_SCAN_SMEM));
-        Q35_CUDA_OK(cudaFuncSetAttribute(pf_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)((ATT_PF_WARPS * ATT_PF_MAX_S + ATT_PF_WARPS * FA_HEAD_DIM) * sizeof(float))));
         Q35_CUDA_OK(cudaFuncSetAttribute(pf_attention_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_MMA_SMEM));
         attr_done = true;
     }
-    static const bool scalar_attention = getenv("QWEN35_PF_SCALAR_ATTENTION") != nullptr;     // the CUDA-core kernel, kept for comparison
     const int nchunks = (S + DN_CHUNK - 1) / DN_CHUNK;
     ChunkScratch* scratch = (ChunkScratch*)get_scratch((size_t)DN_HEADS * nchunks * sizeof(ChunkScratch));
     if (!scratch) return QWEN35_ERR_CUDA;
@@ -113,14 +110,8 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
             bf16* vc = a.v_cache + (size_t)i_fa * FA_KV_HEADS * a.max_seq_len * FA_HEAD_DIM;
             pf_qk_norm_rope_kernel<<<(S * 12 + 7) / 8, 256, 0, stream>>>(a.proj_buf, ldp, (const bf16*)L.p[FA_QNORM], (const bf16*)L.p[FA_KNORM], rt,
                                                                          a.proj_buf2, kc, vc, S, a.max_seq_len);
-            if (scalar_attention) {
-                const size_t att_smem = ((size_t)ATT_PF_WARPS * S + ATT_PF_WARPS * FA_HEAD_DIM) * sizeof(float);
-                pf_attention_kernel<<<dim3((S + ATT_PF_WARPS - 1) / ATT_PF_WARPS, FA_Q_HEADS), ATT_PF_WARPS * 32, att_smem, stream>>>(
-                    a.proj_buf2, kc, vc, a.proj_buf, ldp, a.attn_buf, S, a.max_seq_len);
-            } else {
-                pf_attention_mma_kernel<<<dim3((S + ATT_MMA_Q - 1) / ATT_MMA_Q, FA_KV_HEADS), 256, ATT_MMA_SMEM, stream>>>(
-                    a.proj_buf2, kc, vc, a.proj_buf, ldp, a.attn_buf, S, a.max_seq_len);
-            }
+            pf_attention_mma_kernel<<<dim3((S + ATT_MMA_Q - 1) / ATT_MMA_Q, FA_KV_HEADS), 256, ATT_MMA_SMEM, stream>>>(
+                a.proj_buf2, kc, vc, a.proj_buf, ldp, a.attn_buf, S, a.max_seq_len);
             g_launches.fetch_add(2);
             w_out = (const bf16*)L.p[FA_O]; w_post = (const bf16*)L.p[FA_POST_NORM]; w_down = (const bf16*)L.p[FA_DOWN];
             ++i_fa;

@@ -485,74 +485,11 @@ static __global__ void __launch_bounds__(256) pf_qk_norm_rope_kernel(const bf16*
     for (int i = 0; i < 8; ++i) dst[lane + 32 * i] = f2bf(xv[i]);
 }
 
-// ---- causal GQA attention, exact bf16 rounding points: one warp per (query, head) ----------------------
-// scores = bf16(q.k)/16, softmax in f32 over the whole row, P rounded to bf16, out = bf16(P.V), times bf16(sigmoid(gate)).
-// The row of scores lives in shared memory (S <= ATT_PF_MAX_S).
-constexpr int ATT_PF_MAX_S = 4096;
-constexpr int ATT_PF_WARPS = 8;
+constexpr int ATT_PF_MAX_S = 4096;      // longest prompt the prefill entry points accept
 
-static __global__ void __launch_bounds__(ATT_PF_WARPS * 32) pf_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k_cache,
-                                                                         const bf16* __restrict__ v_cache, const bf16* __restrict__ proj, int ldp,
-                                                                         bf16* __restrict__ out, int S, int max_seq) {
-    extern __shared__ float att_sm[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int head = blockIdx.y, kvh = head / FA_GQA;
-    const int t = (int)gridDim.x * ATT_PF_WARPS - 1 - (blockIdx.x * ATT_PF_WARPS + warp);      // long rows first
-    float* sc = att_sm + (size_t)warp * S;
-    float* sqv = att_sm + (size_t)ATT_PF_WARPS * S + warp * FA_HEAD_DIM;
-    if (t >= S || t < 0) return;
-    for (int i = lane; i < FA_HEAD_DIM; i += 32) sqv[i] = bf2f(q[(size_t)t * FA_Q_SIZE + head * FA_HEAD_DIM + i]);
-    __syncwarp();
-    const bf16* kb = k_cache + (size_t)kvh * max_seq * FA_HEAD_DIM;
-    const bf16* vb = v_cache + (size_t)kvh * max_seq * FA_HEAD_DIM;
-    const int L = t + 1;
-    // pass 1: one key per lane
-    float mx = -INFINITY;
-    for (int j = lane; j < L; j += 32) {
-        const uint4* kr = reinterpret_cast<const uint4*>(kb + (size_t)j * FA_HEAD_DIM);
-        float d = 0.f;
-#pragma unroll 4
-        for (int cidx = 0; cidx < FA_HEAD_DIM / 8; ++cidx) {
-            const uint4 kv = kr[cidx];
-            const float* qq = sqv + cidx * 8;
-            d = fmaf(qq[0], bf_lo(kv.x), d); d = fmaf(qq[1], bf_hi(kv.x), d);
-            d = fmaf(qq[2], bf_lo(kv.y), d); d = fmaf(qq[3], bf_hi(kv.y), d);
-            d = fmaf(qq[4], bf_lo(kv.z), d); d = fmaf(qq[5], bf_hi(kv.z), d);
-            d = fmaf(qq[6], bf_lo(kv.w), d); d = fmaf(qq[7], bf_hi(kv.w), d);
-        }
-        const float s = rbf(d) * 0.0625f;
-        sc[j] = s;
-        mx = fmaxf(mx, s);
-    }
-    mx = warp_max(mx);
-    float sm = 0.f;
-    for (int j = lane; j < L; j += 32) sm += expf(sc[j] - mx);
-    sm = warp_sum(sm);
-    for (int j = lane; j < L; j += 32) sc[j] = rbf(expf(sc[j] - mx) / sm);
-    __syncwarp();
-    // pass 2: eight output dims per lane
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < L; ++j) {
-        const float p = sc[j];
-        const uint4 vv = *(reinterpret_cast<const uint4*>(vb + (size_t)j * FA_HEAD_DIM) + lane);
-        acc[0] = fmaf(p, bf_lo(vv.x), acc[0]); acc[1] = fmaf(p, bf_hi(vv.x), acc[1]);
-        acc[2] = fmaf(p, bf_lo(vv.y), acc[2]); acc[3] = fmaf(p, bf_hi(vv.y), acc[3]);
-        acc[4] = fmaf(p, bf_lo(vv.z), acc[4]); acc[5] = fmaf(p, bf_hi(vv.z), acc[5]);
-        acc[6] = fmaf(p, bf_lo(vv.w), acc[6]); acc[7] = fmaf(p, bf_hi(vv.w), acc[7]);
-    }
-    const uint4 gr = *(reinterpret_cast<const uint4*>(proj + (size_t)t * ldp + head * 2 * FA_HEAD_DIM + FA_HEAD_DIM) + lane);
-    const float gv[8] = {bf_lo(gr.x), bf_hi(gr.x), bf_lo(gr.y), bf_hi(gr.y), bf_lo(gr.z), bf_hi(gr.z), bf_lo(gr.w), bf_hi(gr.w)};
-    uint32_t o[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const __nv_bfloat162 pr = __halves2bfloat162(f2bf(rbf(acc[2 * i]) * rbf(sigmoid_f(gv[2 * i]))),
-                                                     f2bf(rbf(acc[2 * i + 1]) * rbf(sigmoid_f(gv[2 * i + 1]))));
-        o[i] = *reinterpret_cast<const uint32_t*>(&pr);
-    }
-    *(reinterpret_cast<uint4*>(out + (size_t)t * FA_Q_SIZE + head * FA_HEAD_DIM) + lane) = make_uint4(o[0], o[1], o[2], o[3]);
-}
-
-// ---- causal GQA attention on tensor cores (mma.sync m16n8k16 bf16), same rounding points as above -----------
+// ---- causal GQA attention on tensor cores (mma.sync m16n8k16 bf16) ------------------------------------------
+// Rounding points of the bf16 HuggingFace model: scores = bf16(q.k)/16, softmax in f32 over the whole row, P rounded to
+// bf16, out = bf16(P.V), times bf16(sigmoid(gate)).
 // One CTA = 32 queries x the 4 q heads of one kv head = 128 rows (row r: query r/4, head r%4), one 16-row tile per
 // warp, so a K/V chunk staged in shared memory serves all four heads.  Exact softmax in two passes over the causal
 // key range: pass 1 the running row maximum and normaliser from bf16(q.k)/16; pass 2 recomputes the same scores (same
