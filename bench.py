@@ -196,14 +196,14 @@ def tree_verify_bench(dev, n_nodes=33, ctx=4096, iters=5):
             "roofline_frac": alg / (ms * 1e-3) / 1e9 / measured_peak()[0], "tflops": flops / (ms * 1e-3) / 1e12}
 
 
-def batched_decode_bench(weights_gpu, dev, rank, n_seq, ctx, n_steps, kernel_table=False):
+def batched_decode_bench(weights_gpu, dev, rank, n_seq, ctx, n_steps, kernel_table=False, groups=1):
     """Batched-decode configuration: `n_seq` independent sequences per GPU, `ctx`-token contexts prefilled by the library's own
     prefill, `n_steps` greedy steps.  Returns (tok/s on this rank, ms per step, algorithmic bytes per step)."""
     from qwen35_b200.config import QWEN35_0P8B as D
     from qwen35_b200.model import BatchedDecoder
     from qwen35_b200.sharding import sequence_seed
     from qwen35_b200.weights import make_token_ids
-    bd = BatchedDecoder(weights_gpu, batch=n_seq, max_ctx=ctx + n_steps + 64, device=dev)
+    bd = BatchedDecoder(weights_gpu, batch=n_seq, max_ctx=ctx + n_steps + 64, device=dev, groups=groups)
     for sq in range(n_seq):
         bd.prefill(sq, make_token_ids(ctx, sequence_seed(0, rank, sq), D.vocab).to(dev))
     snap = [t.clone() for t in (bd.dn_states, bd.conv_bufs, bd.positions, bd.tokens)]
@@ -425,7 +425,7 @@ def run_ours(args):
         tree = tree_verify_bench(dev)
     batched = None
     if args.batched > 0:
-        b_tok_s, b_ms, b_bytes = batched_decode_bench(wg, dev, rank, args.batched, args.batched_ctx, GEN, kernel_table=args.kernel_table and rank == 0)
+        b_tok_s, b_ms, b_bytes = batched_decode_bench(wg, dev, rank, args.batched, args.batched_ctx, GEN, kernel_table=args.kernel_table and rank == 0, groups=args.batched_groups)
         from qwen35_b200.sharding import reduce_counters
         job = reduce_counters(tokens=args.batched * GEN, elapsed_ms=b_ms * GEN, algorithmic_bytes=b_bytes * GEN, device=dev)
         b_ms = job.elapsed_ms / GEN                         # slowest rank's time per step
@@ -504,6 +504,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batched", type=int, default=64, help="sequences per GPU for the batched-decode section (0 = skip)")
     ap.add_argument("--batched-ctx", type=int, default=2048)
+    ap.add_argument("--batched-groups", type=int, default=1, help="concurrent sub-batches of the batched-decode step (1 = one batch)")
     ap.add_argument("--kernel-table", action="store_true", help="print the per-kernel device times of one batched step to stderr")
     ap.add_argument("--prefill-sweep", default="128,512,1024,4096", help="prompt lengths of the prefill sweep ('' = skip)")
     ap.add_argument("--tree-verify", type=int, default=1, help="run the 27B-class tree-verify section (0 = skip)")

@@ -213,8 +213,11 @@ typedef struct {
     int advance_positions;
     int dbg_num_layers;
     const void* layer_weights_host; const void* fused_layer_weights_host;
+    void* scratch; size_t scratch_bytes;   /* optional caller-owned scratch (256-byte aligned, >= qwen35_b200_batched_scratch_bytes):
+                                              required when two calls run concurrently on two streams; null = the library's own */
 } Qwen35BatchedArgs;
 int qwen35_b200_decode_batched(const Qwen35BatchedArgs* args, qwen35_stream_t stream);
+size_t qwen35_b200_batched_scratch_bytes(int batch, int max_ctx);
 
 /* ---- Tree verification for the 27B-class target (additive: the reference runs this pass as a ggml graph,
  * models/qwen35_27b/src/qwen35_target_graph.cpp:281-804, with the tree logic in models/qwen35_27b/test/test_dflash.cpp).

@@ -397,6 +397,20 @@ const void* host_layer_tables(const void* dev_layers, const void* dev_fused, con
 
 }  // namespace q35
 
+static size_t batched_scratch_total(int batch, int max_ctx) {
+    using namespace q35;
+    const size_t rows = (size_t)batch;
+    const size_t n_hidden = rows * HIDDEN, n_proj = rows * DN_PROJ_ROWS, n_att = rows * 2048, n_mlp = rows * INTER, n_logits = rows * VOCAB;
+    const int max_chunks = (max_ctx + BD_CHUNK - 1) / BD_CHUNK;
+    const size_t n_scores = rows * FA_Q_HEADS * (size_t)max_ctx, n_stats = rows * FA_Q_HEADS * max_chunks * 2, n_part = rows * FA_Q_HEADS * max_chunks * FA_HEAD_DIM;
+    return (3 * n_hidden + n_proj + 3 * n_att + n_mlp + n_logits) * sizeof(bf16) + (n_scores + n_stats + n_part) * sizeof(float) + 4096;
+}
+
+extern "C" size_t qwen35_b200_batched_scratch_bytes(int batch, int max_ctx) {
+    if (batch <= 0 || max_ctx <= 0) return 0;
+    return batched_scratch_total(batch, max_ctx);
+}
+
 #define Q35_TRYB(expr)                       \
     do {                                     \
         const int st__ = (expr);             \
@@ -439,9 +453,18 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
     const int max_chunks = (in->max_ctx + BD_CHUNK - 1) / BD_CHUNK;
     const size_t n_scores = rows * FA_Q_HEADS * (size_t)in->max_ctx, n_stats = rows * FA_Q_HEADS * max_chunks * 2,
                  n_part = rows * FA_Q_HEADS * max_chunks * FA_HEAD_DIM;
-    const size_t total = (3 * n_hidden + n_proj + 3 * n_att + n_mlp + n_logits) * sizeof(bf16) + (n_scores + n_stats + n_part) * sizeof(float) + 4096;
-    char* base = (char*)batched_scratch(total);
-    if (!base) return QWEN35_ERR_CUDA;
+    const size_t total = batched_scratch_total(B, in->max_ctx);
+    char* base;
+    if (in->scratch) {                       // caller-owned scratch: needed when two calls run concurrently on two streams
+        if (in->scratch_bytes < total || ((uintptr_t)in->scratch & 255)) {
+            set_error("batched decode: scratch of %zu bytes given (256-byte aligned?), %zu needed", in->scratch_bytes, total);
+            return QWEN35_ERR_BAD_ARG;
+        }
+        base = (char*)in->scratch;
+    } else {
+        base = (char*)batched_scratch(total);
+        if (!base) return QWEN35_ERR_CUDA;
+    }
     bf16* hidden = (bf16*)base;
     bf16* resid = hidden + n_hidden;
     bf16* normed = resid + n_hidden;

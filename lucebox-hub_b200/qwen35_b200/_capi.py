@@ -56,6 +56,7 @@ class BatchedArgs(C.Structure):
         ("logits_out", C.c_void_p), ("dbg_hidden", C.c_void_p), ("dbg_teacher", C.c_void_p),
         ("advance_positions", C.c_int), ("dbg_num_layers", C.c_int),
         ("layer_weights_host", C.c_void_p), ("fused_layer_weights_host", C.c_void_p),
+        ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t),
     ]
 
 
@@ -96,6 +97,7 @@ SIGNATURES = {
     "launch_quantize_nvfp4_out": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp]),
     "launch_quantize_nvfp4_lm_out": (_i, [_vp, _i, _i, _vp, _vp, _vp]),
     "qwen35_b200_decode_batched": (_i, [C.POINTER(BatchedArgs), _vp]),
+    "qwen35_b200_batched_scratch_bytes": (C.c_size_t, [_i, _i]),
     "qwen35_b200_forget_tables": (None, []),
     "qwen35_b200_draft_topk": (_i, [_vp, _i, _i, _i, C.c_float, _vp, _vp, _vp]),
     "qwen35_b200_build_ddtree": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),

@@ -94,3 +94,22 @@ def test_batched_graph_replay_equals_eager(full_weights_cpu):
         bd.check_status()
         runs.append((outs.cpu(), bd.positions.cpu(), bd.dn_states.cpu()))
     assert torch.equal(runs[0][0], runs[1][0]) and torch.equal(runs[0][1], runs[1][1]) and torch.equal(runs[0][2], runs[1][2])
+
+
+def test_batched_two_concurrent_groups_equal_one_batch(full_weights_cpu):
+    """groups=2 runs the two halves of the batch as concurrent sub-batches (two streams, caller-owned scratch per call):
+    every sequence's tokens, position and state equal the single-batch run."""
+    from qwen35_b200.config import QWEN35_0P8B as D
+    from qwen35_b200.model import BatchedDecoder
+    from qwen35_b200.weights import make_token_ids, weights_to
+    wg = weights_to(full_weights_cpu, "cuda")
+    runs = []
+    for groups in (1, 2):
+        bd = BatchedDecoder(wg, batch=4, max_ctx=192, groups=groups)
+        for b in range(4):
+            bd.prefill(b, make_token_ids(18 + 25 * b, 3 + b, D.vocab).cuda())
+        outs = torch.stack([bd.step(graph=True).clone() for _ in range(5)])
+        bd.check_status()
+        runs.append((outs.cpu(), bd.positions.cpu(), bd.dn_states.cpu(), bd.conv_bufs.cpu()))
+    for a, b in zip(runs[0], runs[1]):
+        assert torch.equal(a, b)
