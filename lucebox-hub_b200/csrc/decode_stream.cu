@@ -87,7 +87,7 @@ struct Smem {
     float hd[2][2];
     __align__(16) float q[FA_GQA][FA_HEAD_DIM];
     __align__(16) float kcur[FA_HEAD_DIM];
-    float p[FA_GQA][ATT_CHUNK_MAX];              // scores, then probabilities, of this CTA's chunk
+    __align__(16) float p[FA_GQA][ATT_CHUNK_MAX]; // scores, then probabilities, of this CTA's chunk; then the merge's group sums
     float ml[FA_GQA][2];
     int abort_flag;
     int tok;
@@ -675,12 +675,14 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                             const int g = tid >> 7, d2 = tid & 127;
                             float acc0 = 0.f, acc1 = 0.f;
                             const uint32_t* vb = reinterpret_cast<const uint32_t*>(vc + ((size_t)kvh * a.max_seq_len + j0) * FA_HEAD_DIM) + d2;
-                            for (int jj = 0; jj < cn; jj += 8) {
-                                uint32_t vr[8];
+                            // 32 value rows in flight: a chunk of up to 32 positions (every context below 2368 tokens)
+                            // costs one L2 round trip, not four
+                            for (int jj = 0; jj < cn; jj += 32) {
+                                uint32_t vr[32];
 #pragma unroll
-                                for (int u = 0; u < 8; ++u) vr[u] = (jj + u < cn) ? ld_cg(vb + (size_t)(jj + u) * (FA_HEAD_DIM / 2)) : 0u;
+                                for (int u = 0; u < 32; ++u) vr[u] = (jj + u < cn) ? ld_cg(vb + (size_t)(jj + u) * (FA_HEAD_DIM / 2)) : 0u;
 #pragma unroll
-                                for (int u = 0; u < 8; ++u) {
+                                for (int u = 0; u < 32; ++u) {
                                     const float p = (jj + u < cn) ? s.p[g][jj + u] : 0.f;
                                     acc0 = fmaf(p, bf_lo(vr[u]), acc0);
                                     acc1 = fmaf(p, bf_hi(vr[u]), acc1);
@@ -702,19 +704,32 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                             }
                         }
                         cons_sync();
+                        {
+                            // 8 groups of 64 threads: group q sums chunks q, q+8, ... (all its loads in flight at once: one L2
+                            // round trip), then thread t < 64 adds the 8 group sums in group order and applies the gate
+                            const int d = (tid & 63) * 4, grp = tid >> 6;
+                            float4 pv[ATT_MAX_CHUNKS / 8];
+#pragma unroll
+                            for (int u = 0; u < ATT_MAX_CHUNKS / 8; ++u) {
+                                const int c = grp + 8 * u;
+                                pv[u] = (c < nchunk) ? ld_cg(reinterpret_cast<const float4*>(&ws->att_part[c][qh][d])) : make_float4(0.f, 0.f, 0.f, 0.f);
+                            }
+                            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                            for (int u = 0; u < ATT_MAX_CHUNKS / 8; ++u) { acc.x += pv[u].x; acc.y += pv[u].y; acc.z += pv[u].z; acc.w += pv[u].w; }
+                            reinterpret_cast<float4*>(&s.p[0][0])[tid] = acc;         // P of this CTA's chunk is no longer needed: [8 groups][64 x float4]
+                        }
+                        cons_sync();
                         if (tid < 64) {
                             const int d = tid * 4;
                             uint32_t g0, g1;
                             const int ge = qh * 2 * FA_HEAD_DIM + FA_HEAD_DIM + d;
                             poll2(&ws->xa[ge >> 1], &ws->xa[(ge >> 1) + 1], ep, ab, g0, g1);
                             float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                            for (int c = 0; c < nchunk; c += 8) {
-                                float4 pv[8];
 #pragma unroll
-                                for (int u = 0; u < 8; ++u)
-                                    pv[u] = (c + u < nchunk) ? ld_cg(reinterpret_cast<const float4*>(&ws->att_part[c + u][qh][d])) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                                for (int u = 0; u < 8; ++u) { acc.x += pv[u].x; acc.y += pv[u].y; acc.z += pv[u].z; acc.w += pv[u].w; }
+                            for (int q = 0; q < 8; ++q) {
+                                const float4 v = reinterpret_cast<const float4*>(&s.p[0][0])[q * 64 + tid];
+                                acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
                             }
                             const float u0 = rbf(acc.x) * rbf(sigmoid_f(bf_lo(g0))), u1 = rbf(acc.y) * rbf(sigmoid_f(bf_hi(g0)));
                             const float u2 = rbf(acc.z) * rbf(sigmoid_f(bf_lo(g1))), u3 = rbf(acc.w) * rbf(sigmoid_f(bf_hi(g1)));
