@@ -499,20 +499,6 @@ constexpr int ATT_PF_MAX_S = 4096;      // longest prompt the prefill entry poin
 constexpr int ATT_MMA_Q = 32, ATT_MMA_ROWS = ATT_MMA_Q * FA_GQA, ATT_MMA_KEYS = 64, ATT_MMA_LD = FA_HEAD_DIM + 8;
 constexpr int ATT_MMA_SMEM = (ATT_MMA_ROWS + 2 * ATT_MMA_KEYS) * ATT_MMA_LD * 2;
 
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
-    const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];" : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
-}
-__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* p) {
-    const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];" : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
-}
-__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
 static __global__ void __launch_bounds__(256, 1) pf_attention_mma_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k_cache,
                                                                   const bf16* __restrict__ v_cache, const bf16* __restrict__ proj, int ldp,
                                                                   bf16* __restrict__ out, int S, int max_seq) {

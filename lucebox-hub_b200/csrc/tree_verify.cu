@@ -185,12 +185,6 @@ __global__ void __launch_bounds__(128) tv_fa_prep_kernel(const bf16* __restrict_
     dst[tid] = f2bf(y[0]); dst[tid + 128] = f2bf(y[1]);
 }
 
-__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
 // scores of all query rows of one kv head (row r = node * gqa + q-in-group) against one chunk of keys:
 // s = (q . k) / 16 in f32, masked to -inf outside [0, past) and the node's ancestors.  grid (chunks, kv_heads).
 __global__ void __launch_bounds__(256, 1) tv_att_scores_kernel(const bf16* __restrict__ qbuf, const bf16* __restrict__ k_cache,
@@ -202,18 +196,20 @@ __global__ void __launch_bounds__(256, 1) tv_att_scores_kernel(const bf16* __res
     bf16* Ks = Qs + (size_t)mt_n * 16 * TV_QSTRIDE;
     const int chunk = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int j0 = chunk * TV_CHUNK, L = past + n_nodes;
+    // Q rows and the K chunk go to shared memory by cp.async: every copy of the tile is in flight at once
     for (int i = tid; i < mt_n * 16 * (TV_HD / 8); i += 256) {
         const int r = i / (TV_HD / 8), c8 = i % (TV_HD / 8);
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (r < R) v = *reinterpret_cast<const uint4*>(qbuf + ((size_t)(r / gqa) * D.q_heads + kvh * gqa + r % gqa) * TV_HD + c8 * 8);
-        *reinterpret_cast<uint4*>(Qs + (size_t)r * TV_QSTRIDE + c8 * 8) = v;
+        bf16* dst = Qs + (size_t)r * TV_QSTRIDE + c8 * 8;
+        if (r < R) cp_async16(dst, qbuf + ((size_t)(r / gqa) * D.q_heads + kvh * gqa + r % gqa) * TV_HD + c8 * 8);
+        else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
     }
     for (int i = tid; i < TV_CHUNK * (TV_HD / 8); i += 256) {
         const int k = i / (TV_HD / 8), c8 = i % (TV_HD / 8);
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (j0 + k < L) v = *reinterpret_cast<const uint4*>(k_cache + ((size_t)kvh * max_ctx + j0 + k) * TV_HD + c8 * 8);
-        *reinterpret_cast<uint4*>(Ks + (size_t)k * TV_QSTRIDE + c8 * 8) = v;
+        bf16* dst = Ks + (size_t)k * TV_QSTRIDE + c8 * 8;
+        if (j0 + k < L) cp_async16(dst, k_cache + ((size_t)kvh * max_ctx + j0 + k) * TV_HD + c8 * 8);
+        else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
     }
+    cp_async_wait_all();
     __syncthreads();
     const int g = lane >> 2, c = lane & 3;
     for (int nt = warp; nt < TV_CHUNK / 8; nt += 8) {
@@ -235,7 +231,7 @@ __global__ void __launch_bounds__(256, 1) tv_att_scores_kernel(const bf16* __res
                 a[1] = *reinterpret_cast<const uint32_t*>(q1 + s * 16);
                 a[2] = *reinterpret_cast<const uint32_t*>(q0 + s * 16 + 8);
                 a[3] = *reinterpret_cast<const uint32_t*>(q1 + s * 16 + 8);
-                mma_bf16_16816(acc, a, bfr[s][0], bfr[s][1]);
+                mma_16816(acc, a, bfr[s][0], bfr[s][1]);
             }
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -268,28 +264,24 @@ __global__ void __launch_bounds__(256) tv_att_stats_kernel(const float* __restri
     if (lane == 0) { stats[2 * r] = mx; stats[2 * r + 1] = sm; }
 }
 
-// partial P.V of one chunk of keys for all query rows of one kv head; P = bf16(exp(s - m) / l).  grid (chunks, kv_heads)
+// partial P.V of one chunk of keys for all query rows of one kv head; P = bf16(exp(s - m) / l).  grid (chunks, kv_heads).
+// The V chunk is staged row-major by cp.async and read as the B operand with ldmatrix.trans; P goes to shared memory
+// row-major and is read as the A operand with ldmatrix.
 __global__ void __launch_bounds__(256, 1) tv_att_pv_kernel(const bf16* __restrict__ v_cache, const float* __restrict__ scores, const float* __restrict__ stats,
                                                            TvDims D, int n_nodes, int past, int max_ctx, int lpad, float* __restrict__ partial) {
     extern __shared__ __align__(16) unsigned char tv_smem[];
-    bf16* Vt = reinterpret_cast<bf16*>(tv_smem);                     // [256 dims][TV_PSTRIDE keys]
-    bf16* Ps = Vt + (size_t)TV_HD * TV_PSTRIDE;                      // [rows][TV_PSTRIDE keys]
+    bf16* Vs = reinterpret_cast<bf16*>(tv_smem);                     // [TV_CHUNK keys][TV_QSTRIDE]
+    bf16* Ps = Vs + (size_t)TV_CHUNK * TV_QSTRIDE;                   // [rows][TV_PSTRIDE keys]
     const int gqa = D.q_heads / D.kv_heads, R = n_nodes * gqa, mt_n = (R + 15) / 16;
     const int chunk = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int j0 = chunk * TV_CHUNK, L = past + n_nodes;
-    // V chunk transposed: lane <-> key, 8 dims at a time
     for (int i = tid; i < TV_CHUNK * (TV_HD / 8); i += 256) {
-        const int k = i % TV_CHUNK, c8 = i / TV_CHUNK;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (j0 + k < L) v = *reinterpret_cast<const uint4*>(v_cache + ((size_t)kvh * max_ctx + j0 + k) * TV_HD + c8 * 8);
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            Vt[(size_t)(c8 * 8 + 2 * e) * TV_PSTRIDE + k] = __ushort_as_bfloat16((unsigned short)(w[e] & 0xFFFF));
-            Vt[(size_t)(c8 * 8 + 2 * e + 1) * TV_PSTRIDE + k] = __ushort_as_bfloat16((unsigned short)(w[e] >> 16));
-        }
+        const int k = i / (TV_HD / 8), c8 = i % (TV_HD / 8);
+        bf16* dst = Vs + (size_t)k * TV_QSTRIDE + c8 * 8;
+        if (j0 + k < L) cp_async16(dst, v_cache + ((size_t)kvh * max_ctx + j0 + k) * TV_HD + c8 * 8);
+        else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
     }
-    for (int i = tid; i < mt_n * 16 * TV_CHUNK; i += 256) {
+    for (int i = tid; i < mt_n * 16 * TV_CHUNK; i += 256) {           // overlaps the copies above
         const int r = i / TV_CHUNK, k = i % TV_CHUNK;
         float p = 0.f;
         if (r < R) {
@@ -299,35 +291,32 @@ __global__ void __launch_bounds__(256, 1) tv_att_pv_kernel(const bf16* __restric
         }
         Ps[(size_t)r * TV_PSTRIDE + k] = f2bf(p);
     }
+    cp_async_wait_all();
     __syncthreads();
     const int g = lane >> 2, c = lane & 3;
     const int n_chunks = gridDim.x;
-    for (int nt = warp; nt < TV_HD / 8; nt += 8) {
-        uint32_t bfr[TV_CHUNK / 16][2];
-        const bf16* vr = Vt + (size_t)(nt * 8 + g) * TV_PSTRIDE + 2 * c;
+    for (int np = warp; np < TV_HD / 16; np += 8) {                   // pairs of 8-dim output tiles
+        uint32_t bfr[TV_CHUNK / 16][4];
 #pragma unroll
-        for (int s = 0; s < TV_CHUNK / 16; ++s) {
-            bfr[s][0] = *reinterpret_cast<const uint32_t*>(vr + s * 16);
-            bfr[s][1] = *reinterpret_cast<const uint32_t*>(vr + s * 16 + 8);
-        }
+        for (int s = 0; s < TV_CHUNK / 16; ++s)
+            ldsm_x4_trans(bfr[s], Vs + (size_t)(s * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * TV_QSTRIDE + np * 16 + 8 * (lane >> 4));
         for (int mt = 0; mt < mt_n; ++mt) {
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            const bf16* p0 = Ps + (size_t)(mt * 16 + g) * TV_PSTRIDE + 2 * c;
-            const bf16* p1 = p0 + 8 * TV_PSTRIDE;
+            float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int s = 0; s < TV_CHUNK / 16; ++s) {
                 uint32_t a[4];
-                a[0] = *reinterpret_cast<const uint32_t*>(p0 + s * 16);
-                a[1] = *reinterpret_cast<const uint32_t*>(p1 + s * 16);
-                a[2] = *reinterpret_cast<const uint32_t*>(p0 + s * 16 + 8);
-                a[3] = *reinterpret_cast<const uint32_t*>(p1 + s * 16 + 8);
-                mma_bf16_16816(acc, a, bfr[s][0], bfr[s][1]);
+                ldsm_x4(a, Ps + (size_t)(mt * 16 + (lane & 15)) * TV_PSTRIDE + s * 16 + (lane >> 4) * 8);
+                mma_16816(acc0, a, bfr[s][0], bfr[s][1]);
+                mma_16816(acc1, a, bfr[s][2], bfr[s][3]);
             }
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const int r = mt * 16 + g + 8 * h;
-                if (r < R)
-                    *reinterpret_cast<float2*>(partial + (((size_t)kvh * R + r) * n_chunks + chunk) * TV_HD + nt * 8 + 2 * c) = make_float2(acc[2 * h], acc[2 * h + 1]);
+                if (r < R) {
+                    float* dst = partial + (((size_t)kvh * R + r) * n_chunks + chunk) * TV_HD + np * 16 + 2 * c;
+                    *reinterpret_cast<float2*>(dst) = make_float2(acc0[2 * h], acc0[2 * h + 1]);
+                    *reinterpret_cast<float2*>(dst + 8) = make_float2(acc1[2 * h], acc1[2 * h + 1]);
+                }
             }
         }
     }
@@ -405,33 +394,54 @@ __global__ void __launch_bounds__(128) tv_dn_tree_kernel(const float* __restrict
                                                          const int* __restrict__ parents, int n_nodes, TvDims D,
                                                          const float* __restrict__ ssm_state, __half* __restrict__ node_states,
                                                          float* __restrict__ core) {
-    const int h = blockIdx.x, rb = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // every node's q, k, 16 values and gate pair are staged in shared memory up front (all copies in flight together),
+    // so the node loop carries only the state recurrence and the occasional parent-state reload
+    __shared__ __align__(16) float sq[TV_MAX_NODES][TV_DN];
+    __shared__ __align__(16) float sk[TV_MAX_NODES][TV_DN];
+    __shared__ __align__(16) float sv[TV_MAX_NODES][16];
+    __shared__ float sg[TV_MAX_NODES][2];
+    __shared__ int sp[TV_MAX_NODES];
+    const int h = blockIdx.x, rb = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int kh = h % D.dn_k_heads;
     const size_t head_elems = (size_t)TV_DN * TV_DN;
     const int v0 = rb * 16 + warp * 4;
+    for (int i = tid; i < n_nodes * (TV_DN / 4); i += 128) {
+        const int t = i / (TV_DN / 4), l = i % (TV_DN / 4);
+        const float* row = qkv + (size_t)t * conv_ch;
+        cp_async16(&sq[t][l * 4], row + kh * TV_DN + l * 4);
+        cp_async16(&sk[t][l * 4], row + (D.dn_k_heads + kh) * TV_DN + l * 4);
+    }
+    for (int i = tid; i < n_nodes * 4; i += 128)
+        cp_async16(&sv[i >> 2][(i & 3) * 4], qkv + (size_t)(i >> 2) * conv_ch + 2 * D.dn_k_heads * TV_DN + h * TV_DN + rb * 16 + (i & 3) * 4);
+    for (int i = tid; i < n_nodes * 2; i += 128) sg[i >> 1][i & 1] = gate[((size_t)(i >> 1) * D.dn_v_heads + h) * 2 + (i & 1)];
+    for (int i = tid; i < n_nodes; i += 128) sp[i] = parents[i];
+    cp_async_wait_all();
+    __syncthreads();
     float4 st[4];
     for (int t = 0; t < n_nodes; ++t) {
-        const int p = parents[t];
+        const int p = sp[t];
         if (t == 0 || p != t - 1) {
             if (p < 0) {
 #pragma unroll
                 for (int r = 0; r < 4; ++r) st[r] = *(reinterpret_cast<const float4*>(ssm_state + (size_t)h * head_elems + (size_t)(v0 + r) * TV_DN) + lane);
             } else {
+                uint2 raw[4];
+#pragma unroll
+                for (int r = 0; r < 4; ++r)
+                    raw[r] = *(reinterpret_cast<const uint2*>(node_states + ((size_t)p * D.dn_v_heads + h) * head_elems + (size_t)(v0 + r) * TV_DN) + lane);
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
-                    const uint2 raw = *(reinterpret_cast<const uint2*>(node_states + ((size_t)p * D.dn_v_heads + h) * head_elems + (size_t)(v0 + r) * TV_DN) + lane);
-                    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x)), b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+                    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw[r].x)), b = __half22float2(*reinterpret_cast<const __half2*>(&raw[r].y));
                     st[r] = make_float4(a.x, a.y, b.x, b.y);
                 }
             }
         }
-        const float* row = qkv + (size_t)t * conv_ch;
-        const float4 q4 = *(reinterpret_cast<const float4*>(row + kh * TV_DN) + lane);
-        const float4 k4 = *(reinterpret_cast<const float4*>(row + (D.dn_k_heads + kh) * TV_DN) + lane);
-        const float beta = gate[((size_t)t * D.dn_v_heads + h) * 2], decay = gate[((size_t)t * D.dn_v_heads + h) * 2 + 1];
+        const float4 q4 = *(reinterpret_cast<const float4*>(sq[t]) + lane);
+        const float4 k4 = *(reinterpret_cast<const float4*>(sk[t]) + lane);
+        const float beta = sg[t][0], decay = sg[t][1];
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-            const float vv = row[2 * D.dn_k_heads * TV_DN + h * TV_DN + v0 + r];
+            const float vv = sv[t][warp * 4 + r];
             float4 u = st[r];
             u.x = __fmul_rn(u.x, decay); u.y = __fmul_rn(u.y, decay); u.z = __fmul_rn(u.z, decay); u.w = __fmul_rn(u.w, decay);
             float kv = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(u.x, k4.x), __fmul_rn(u.y, k4.y)), __fmul_rn(u.z, k4.z)), __fmul_rn(u.w, k4.w));
@@ -667,7 +677,7 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
     const int chunks = (L + TV_CHUNK - 1) / TV_CHUNK;          // chunks that hold visible keys
     const int R = n * gqa, mt_n = (R + 15) / 16;
     const size_t sc_smem = ((size_t)mt_n * 16 * TV_QSTRIDE + (size_t)TV_CHUNK * TV_QSTRIDE) * 2;
-    const size_t pv_smem = ((size_t)TV_HD * TV_PSTRIDE + (size_t)mt_n * 16 * TV_PSTRIDE) * 2;
+    const size_t pv_smem = ((size_t)TV_CHUNK * TV_QSTRIDE + (size_t)mt_n * 16 * TV_PSTRIDE) * 2;
     static bool attr_done = false;
     if (!attr_done) {
         Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
