@@ -477,59 +477,76 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
             umma_commit(tfull);
         }
     } else {
-        // ---- dequantisation: thread (row, h, part) converts half of group h (16 nibble bytes = 32 weights: chunks
-        // 2*part, 2*part+1 from the low nibbles, 4+2*part, 5+2*part from the high ones) of every k-step ----
+        // ---- dequantisation: thread (row, h, part) converts half of group 2*par + h of k-step `par` of every super-block
+        // (16 nibble bytes = 32 weights: chunks 2*part, 2*part+1 from the low nibbles, 4+2*part, 5+2*part from the high
+        // ones).  The loop runs per super-block with the k-step parity known at compile time: the 6-bit scale decoding
+        // is branch-free, the header is read once for both k-steps, and ring positions advance by counters. ----
         const int dw = warp - 2, row = (dw & 3) * 32 + lane, h = (dw >> 2) & 1, part = dw >> 3;
+        const int sh = 16 * h;
+        uint32_t off[4];
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) off[cc] = (uint32_t)(((((cc >= 2) ? 4 : 0) + 2 * part + (cc & 1)) ^ (row & 7)) << 4);
+        unsigned char* const bbase = tiles_ptr + 2 * Q4K_A_SLAB + h * Q4K_B_SLAB + row * 128;
+        const unsigned char* const rbase = rawring_ptr + row * 144;
+        const __nv_bfloat162 k128 = __float2bfloat162_rn(128.0f);
+        int st = 0, rs = 0;
+        uint32_t st_par = 1, rs_par = 0;
+        const int nsb = sb_end - sb_begin;
         bool alive = true;
-        for (int i = 0; i < nk2 && alive; ++i) {
-            const int st = i % STAGES, j = i >> 1, rs = j % RS;
-            int okw = 1;
-            if (lane == 0)
-                okw = (g_mbar_wait(fullr0 + 8 * rs, (j / RS) & 1, p.err, s_abort) && g_mbar_wait(empty0 + 8 * st, ((i / STAGES) & 1) ^ 1, p.err, s_abort)) ? 1 : 0;
-            alive = __shfl_sync(0xffffffffu, okw, 0) != 0;
+        for (int j = 0; j < nsb && alive; ++j) {
+            alive = __all_sync(0xffffffffu, g_mbar_wait(fullr0 + 8 * rs, rs_par, p.err, s_abort));
             if (!alive) break;
-            const unsigned char* rb = rawring_ptr + rs * Q4K_RAW_BYTES + row * 144;
-            const int g = 2 * (i & 1) + h;
+            const unsigned char* rb = rbase + rs * Q4K_RAW_BYTES;
             const uint4 hd = *reinterpret_cast<const uint4*>(rb);
-            const uint4 qv = *reinterpret_cast<const uint4*>(rb + 16 + 32 * g + 16 * part);
             const __half2 dd = *reinterpret_cast<const __half2*>(&hd.x);
-            const float d = __low2float(dd), dmin = __high2float(dd);
-            float sc0, m0, sc1, m1;
-            q4k_scale_min_u32(hd.y, hd.z, hd.w, 2 * g, sc0, m0);
-            q4k_scale_min_u32(hd.y, hd.z, hd.w, 2 * g + 1, sc1, m1);
-            // operand value = bf16 fma(q, bf16(d*sc), -bf16(dmin*m)): d*sc and dmin*m are exact in f32 (11 + 6 bits), one
-            // rounding each to bf16, then one fused rounding; two weights per instruction
-            const __nv_bfloat162 ds0 = __float2bfloat162_rn(__fmul_rn(d, sc0)), ds1 = __float2bfloat162_rn(__fmul_rn(d, sc1));
-            const __nv_bfloat162 nm0 = __hneg2(__float2bfloat162_rn(__fmul_rn(dmin, m0))), nm1 = __hneg2(__float2bfloat162_rn(__fmul_rn(dmin, m1)));
-            const __nv_bfloat162 k128 = __float2bfloat162_rn(128.0f);
-            const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
-            unsigned char* brow = tiles_ptr + st * Q4K_STAGE_BYTES + 2 * Q4K_A_SLAB + h * Q4K_B_SLAB + row * 128;
+            const float d = __low2float(dd), ndmin = -__high2float(dd);
+            const uint32_t sx = hd.y >> sh, sy = hd.z >> sh, sz = hd.w >> sh;      // scale bytes 2h.., 4+2h.., 8+2h..
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {                    // cc 0,1: low nibbles; 2,3: high nibbles
-                const bool hi = cc >= 2;
-                const int c = (hi ? 4 : 0) + 2 * part + (cc & 1);     // chunk = weights 8c..8c+7 of the group
-                const __nv_bfloat162 dsx = hi ? ds1 : ds0, nmx = hi ? nm1 : nm0;
-                uint32_t o[4];
-#pragma unroll
-                for (int h2 = 0; h2 < 2; ++h2) {
-                    const uint32_t word = w[2 * (cc & 1) + h2];
-                    const uint32_t nib = (hi ? (word >> 4) : word) & 0x0F0F0F0Fu;
-                    // bytes (q, 0x43) are the bf16 numbers 128 + q: exact, no integer conversion
-                    const uint32_t u01 = __byte_perm(nib, 0x43004300u, 0x7150), u23 = __byte_perm(nib, 0x43004300u, 0x7352);
-                    const __nv_bfloat162 x01 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&u01), k128);
-                    const __nv_bfloat162 x23 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&u23), k128);
-                    const __nv_bfloat162 y01 = __hfma2(x01, dsx, nmx), y23 = __hfma2(x23, dsx, nmx);
-                    o[2 * h2] = *reinterpret_cast<const uint32_t*>(&y01);
-                    o[2 * h2 + 1] = *reinterpret_cast<const uint32_t*>(&y23);
+            for (int par = 0; par < 2; ++par) {
+                alive = __all_sync(0xffffffffu, g_mbar_wait(empty0 + 8 * st, st_par, p.err, s_abort));
+                if (!alive) break;
+                const uint4 qv = *reinterpret_cast<const uint4*>(rb + 16 + 32 * (2 * par + h) + 16 * part);
+                uint32_t sc0, mn0, sc1, mn1;                                        // sub-blocks 2g and 2g+1 of group g = 2*par + h
+                if (par == 0) {
+                    sc0 = sx & 63u; sc1 = (sx >> 8) & 63u; mn0 = sy & 63u; mn1 = (sy >> 8) & 63u;
+                } else {
+                    sc0 = (sz & 0xFu) | ((sx >> 2) & 0x30u);         mn0 = ((sz >> 4) & 0xFu) | ((sy >> 2) & 0x30u);
+                    sc1 = ((sz >> 8) & 0xFu) | ((sx >> 10) & 0x30u); mn1 = ((sz >> 12) & 0xFu) | ((sy >> 10) & 0x30u);
                 }
-                *reinterpret_cast<uint4*>(brow + ((c ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                // operand value = bf16 fma(q, bf16(d*sc), -bf16(dmin*m)): d*sc and dmin*m are exact in f32 (11 + 6 bits), one
+                // rounding each to bf16 (round-to-nearest is symmetric, so the sign goes in before it), then one fused rounding
+                const __nv_bfloat162 ds0 = __float2bfloat162_rn(__fmul_rn(d, (float)sc0)), ds1 = __float2bfloat162_rn(__fmul_rn(d, (float)sc1));
+                const __nv_bfloat162 nm0 = __float2bfloat162_rn(__fmul_rn(ndmin, (float)mn0)), nm1 = __float2bfloat162_rn(__fmul_rn(ndmin, (float)mn1));
+                const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
+                unsigned char* brow = bbase + st * Q4K_STAGE_BYTES;
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {                    // cc 0,1: low nibbles; 2,3: high nibbles
+                    const bool hi = cc >= 2;
+                    const __nv_bfloat162 dsx = hi ? ds1 : ds0, nmx = hi ? nm1 : nm0;
+                    uint32_t o[4];
+#pragma unroll
+                    for (int h2 = 0; h2 < 2; ++h2) {
+                        const uint32_t word = w[2 * (cc & 1) + h2];
+                        const uint32_t nib = (hi ? (word >> 4) : word) & 0x0F0F0F0Fu;
+                        // bytes (q, 0x43) are the bf16 numbers 128 + q: exact, no integer conversion
+                        const uint32_t u01 = __byte_perm(nib, 0x43004300u, 0x7150), u23 = __byte_perm(nib, 0x43004300u, 0x7352);
+                        const __nv_bfloat162 x01 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&u01), k128);
+                        const __nv_bfloat162 x23 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&u23), k128);
+                        const __nv_bfloat162 y01 = __hfma2(x01, dsx, nmx), y23 = __hfma2(x23, dsx, nmx);
+                        o[2 * h2] = *reinterpret_cast<const uint32_t*>(&y01);
+                        o[2 * h2 + 1] = *reinterpret_cast<const uint32_t*>(&y23);
+                    }
+                    *reinterpret_cast<uint4*>(brow + off[cc]) = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");      // generic-proxy writes -> visible to the MMA
+                __syncwarp();
+                if (lane == 0) {
+                    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(fullb0 + 8 * st) : "memory");
+                    if (par == 1) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(emptyr0 + 8 * rs) : "memory");   // super-block consumed
+                }
+                if (++st == STAGES) { st = 0; st_par ^= 1u; }
             }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");      // generic-proxy writes -> visible to the MMA
-            __syncwarp();
-            if (lane == 0) {
-                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(fullb0 + 8 * st) : "memory");
-                if (i & 1) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(emptyr0 + 8 * rs) : "memory");   // super-block consumed
-            }
+            if (++rs == RS) { rs = 0; rs_par ^= 1u; }
         }
         if (warp < 6) {
             // ---- epilogue part 1: park the f32 tile column-major in the idle stage buffers ----

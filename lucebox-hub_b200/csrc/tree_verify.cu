@@ -106,13 +106,41 @@ __global__ void __launch_bounds__(32) tv_embed_q4k_kernel(const uint8_t* __restr
 
 // ------------------------------------------- tree bookkeeping -------------------------------------------
 // depth[t] and the ancestor-or-self word anc[t] (bit j set: node j is on the root-to-t path); parents[t] < t.
-__global__ void tv_tree_prep_kernel(const int* __restrict__ parents, int n, int* __restrict__ depth, unsigned long long* __restrict__ anc) {
+// For the tree delta rule it also plans where each node's starting state comes from and which post-states a CTA keeps
+// in one of its TV_DN_SLOTS shared-memory slots:
+//   src[t]  = -2 continue from node t-1's registers; -1 read from memory (the parent's persisted state, or the
+//             committed state for a root); s >= 0 read the parent's state from slot s
+//   save[t] = slot that keeps node t's post-state for a later child that is not t+1, or -1
+// A slot is held from its node until that node's last such child; when none is free the child reads from memory.
+constexpr int TV_DN_SLOTS = 8;
+__global__ void tv_tree_prep_kernel(const int* __restrict__ parents, int n, int* __restrict__ depth, unsigned long long* __restrict__ anc,
+                                    int* __restrict__ src, int* __restrict__ save) {
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    int last[TV_MAX_NODES], owner[TV_DN_SLOTS];
     for (int t = 0; t < n; ++t) {
         const int p = parents[t];
         const bool ok = p >= 0 && p < t;
         depth[t] = ok ? depth[p] + 1 : 0;
         anc[t] = (ok ? anc[p] : 0ull) | (1ull << t);
+        last[t] = -1;
+    }
+    for (int c = 1; c < n; ++c) {
+        const int p = parents[c];
+        if (p >= 0 && p < c && p != c - 1) last[p] = c;
+    }
+    for (int i = 0; i < TV_DN_SLOTS; ++i) owner[i] = -1;
+    for (int t = 0; t < n; ++t) {
+        const int p = parents[t];
+        int from = -1;
+        if (t > 0 && p == t - 1) from = -2;
+        else if (p >= 0 && p < t)
+            for (int i = 0; i < TV_DN_SLOTS; ++i) if (owner[i] == p) from = i;
+        src[t] = from;
+        for (int i = 0; i < TV_DN_SLOTS; ++i) if (owner[i] >= 0 && last[owner[i]] <= t) owner[i] = -1;
+        int keep = -1;
+        if (last[t] > t)
+            for (int i = 0; i < TV_DN_SLOTS && keep < 0; ++i) if (owner[i] < 0) { owner[i] = t; keep = i; }
+        save[t] = keep;
     }
 }
 
@@ -239,12 +267,14 @@ __global__ void __launch_bounds__(256, 1) tv_att_scores_kernel(const bf16* __res
                 if (r >= R) continue;
                 const unsigned long long am = anc[r / gqa];
                 float* dst = scores + ((size_t)kvh * R + r) * lpad + j0 + nt * 8 + 2 * c;
+                float2 out;
 #pragma unroll
                 for (int e = 0; e < 2; ++e) {
                     const int j = j0 + nt * 8 + 2 * c + e;
                     const bool vis = j < past || (j < L && ((am >> (j - past)) & 1ull));
-                    dst[e] = vis ? acc[2 * h + e] * 0.0625f : -INFINITY;
+                    (e ? out.y : out.x) = vis ? acc[2 * h + e] * 0.0625f : -INFINITY;
                 }
+                *reinterpret_cast<float2*>(dst) = out;
             }
         }
     }
@@ -255,11 +285,20 @@ __global__ void __launch_bounds__(256) tv_att_stats_kernel(const float* __restri
     const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (r >= rows) return;
     const float* s = scores + (size_t)r * lpad;
+    // len is a multiple of the 128-key chunk: 16-byte loads, element order of the sum = (lane, then key) as before per lane
     float mx = -INFINITY;
-    for (int j = lane; j < len; j += 32) mx = fmaxf(mx, s[j]);
+#pragma unroll 4
+    for (int j = lane * 4; j < len; j += 128) {
+        const float4 v = *reinterpret_cast<const float4*>(s + j);
+        mx = fmaxf(fmaxf(mx, fmaxf(v.x, v.y)), fmaxf(v.z, v.w));
+    }
     mx = warp_max(mx);
     float sm = 0.f;
-    for (int j = lane; j < len; j += 32) sm += expf(s[j] - mx);
+#pragma unroll 4
+    for (int j = lane * 4; j < len; j += 128) {
+        const float4 v = *reinterpret_cast<const float4*>(s + j);
+        sm += expf(v.x - mx); sm += expf(v.y - mx); sm += expf(v.z - mx); sm += expf(v.w - mx);
+    }
     sm = warp_sum(sm);
     if (lane == 0) { stats[2 * r] = mx; stats[2 * r + 1] = sm; }
 }
@@ -281,15 +320,22 @@ __global__ void __launch_bounds__(256, 1) tv_att_pv_kernel(const bf16* __restric
         if (j0 + k < L) cp_async16(dst, v_cache + ((size_t)kvh * max_ctx + j0 + k) * TV_HD + c8 * 8);
         else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
     }
-    for (int i = tid; i < mt_n * 16 * TV_CHUNK; i += 256) {           // overlaps the copies above
-        const int r = i / TV_CHUNK, k = i % TV_CHUNK;
-        float p = 0.f;
+    // P rows (overlapping the copies above): a warp takes one row at a time, a lane four consecutive keys, so the score
+    // loads are 16-byte, coalesced and several rows deep in flight
+    static_assert(TV_CHUNK == 128, "one warp covers a 128-key row with four keys per lane");
+#pragma unroll 4
+    for (int r = warp; r < mt_n * 16; r += 8) {
+        float4 sc = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        float m = 0.f, l = 1.f;
         if (r < R) {
             const size_t gr = (size_t)kvh * R + r;
-            const float s = scores[gr * lpad + j0 + k];
-            p = (s == -INFINITY) ? 0.f : expf(s - stats[2 * gr]) / stats[2 * gr + 1];
+            sc = *reinterpret_cast<const float4*>(scores + gr * lpad + j0 + lane * 4);
+            m = stats[2 * gr]; l = stats[2 * gr + 1];
         }
-        Ps[(size_t)r * TV_PSTRIDE + k] = f2bf(p);
+        const float p0 = (sc.x == -INFINITY) ? 0.f : expf(sc.x - m) / l, p1 = (sc.y == -INFINITY) ? 0.f : expf(sc.y - m) / l;
+        const float p2 = (sc.z == -INFINITY) ? 0.f : expf(sc.z - m) / l, p3 = (sc.w == -INFINITY) ? 0.f : expf(sc.w - m) / l;
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(p0, p1), hi = __floats2bfloat162_rn(p2, p3);
+        *reinterpret_cast<uint2*>(Ps + (size_t)r * TV_PSTRIDE + lane * 4) = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
     }
     cp_async_wait_all();
     __syncthreads();
@@ -386,77 +432,106 @@ __global__ void __launch_bounds__(128) tv_dn_norm_kernel(float* __restrict__ qkv
     }
 }
 
-// tree gated delta rule: one CTA (4 warps x 4 value rows) per (v head, block of 16 value rows); nodes in DFS order.
-// The running f32 state continues from node t-1 when that is the parent, else it is reloaded from the parent's
-// persisted f16 post-state (or the committed f32 state for a child of nothing).  Every node's post-state is
-// persisted as f16 (qwen35_target_graph.cpp:540-583).  v head h uses k head h % k_heads (ggml_repeat tiling, :531-534).
+// tree gated delta rule: one CTA of 128 threads per (v head, block of 16 value rows); nodes in the given order.
+// Thread (row, slice) owns 16 state elements of one value row (float4 number slice + 8 i, i = 0..3), so a row's dot
+// products reduce over 8 lanes.  Every node's q, k, 16 values and gate pair are staged in shared memory up front.
+// The running f32 state continues from node t-1 when that is the parent; otherwise it restarts from the parent's
+// persisted f16 post-state (a thread-private copy in a shared-memory slot when tv_tree_prep planned one, else global
+// memory), or from the committed f32 state for a root.  Every node's post-state is persisted as f16
+// (qwen35_target_graph.cpp:540-583).  v head h uses k head h % k_heads (ggml_repeat tiling, :531-534).
+__host__ __device__ constexpr size_t tv_dn_tree_smem(int n) {
+    return ((size_t)n * (2 * TV_DN + 16 + 2) * 4 + (size_t)n * 3 * 4 + 15) / 16 * 16 + (size_t)TV_DN_SLOTS * 4 * 128 * 8;
+}
+__device__ __forceinline__ float dot4_rn(const float4& a, const float4& b) {
+    return __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y)), __fmul_rn(a.z, b.z)), __fmul_rn(a.w, b.w));
+}
 __global__ void __launch_bounds__(128) tv_dn_tree_kernel(const float* __restrict__ qkv, int conv_ch, const float* __restrict__ gate,
-                                                         const int* __restrict__ parents, int n_nodes, TvDims D,
-                                                         const float* __restrict__ ssm_state, __half* __restrict__ node_states,
+                                                         const int* __restrict__ parents, const int* __restrict__ src, const int* __restrict__ save,
+                                                         int n_nodes, TvDims D, const float* __restrict__ ssm_state, __half* __restrict__ node_states,
                                                          float* __restrict__ core) {
-    // every node's q, k, 16 values and gate pair are staged in shared memory up front (all copies in flight together),
-    // so the node loop carries only the state recurrence and the occasional parent-state reload
-    __shared__ __align__(16) float sq[TV_MAX_NODES][TV_DN];
-    __shared__ __align__(16) float sk[TV_MAX_NODES][TV_DN];
-    __shared__ __align__(16) float sv[TV_MAX_NODES][16];
-    __shared__ float sg[TV_MAX_NODES][2];
-    __shared__ int sp[TV_MAX_NODES];
-    const int h = blockIdx.x, rb = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    extern __shared__ __align__(16) unsigned char tv_smem[];
+    float* sq = reinterpret_cast<float*>(tv_smem);                       // [n][128]
+    float* sk = sq + (size_t)n_nodes * TV_DN;                             // [n][128]
+    float* sv = sk + (size_t)n_nodes * TV_DN;                             // [n][16]
+    float* sg = sv + (size_t)n_nodes * 16;                                // [n][2]
+    int* sp = reinterpret_cast<int*>(sg + (size_t)n_nodes * 2);           // [n] parent, [n] source, [n] slot to keep
+    int* ssrc = sp + n_nodes;
+    int* ssave = ssrc + n_nodes;
+    uint2* slots = reinterpret_cast<uint2*>(tv_smem + tv_dn_tree_smem(n_nodes) - (size_t)TV_DN_SLOTS * 4 * 128 * 8);   // [slot][i][thread]
+    const int h = blockIdx.x, rb = blockIdx.y, tid = threadIdx.x;
     const int kh = h % D.dn_k_heads;
     const size_t head_elems = (size_t)TV_DN * TV_DN;
-    const int v0 = rb * 16 + warp * 4;
     for (int i = tid; i < n_nodes * (TV_DN / 4); i += 128) {
         const int t = i / (TV_DN / 4), l = i % (TV_DN / 4);
         const float* row = qkv + (size_t)t * conv_ch;
-        cp_async16(&sq[t][l * 4], row + kh * TV_DN + l * 4);
-        cp_async16(&sk[t][l * 4], row + (D.dn_k_heads + kh) * TV_DN + l * 4);
+        cp_async16(sq + (size_t)t * TV_DN + l * 4, row + kh * TV_DN + l * 4);
+        cp_async16(sk + (size_t)t * TV_DN + l * 4, row + (D.dn_k_heads + kh) * TV_DN + l * 4);
     }
     for (int i = tid; i < n_nodes * 4; i += 128)
-        cp_async16(&sv[i >> 2][(i & 3) * 4], qkv + (size_t)(i >> 2) * conv_ch + 2 * D.dn_k_heads * TV_DN + h * TV_DN + rb * 16 + (i & 3) * 4);
-    for (int i = tid; i < n_nodes * 2; i += 128) sg[i >> 1][i & 1] = gate[((size_t)(i >> 1) * D.dn_v_heads + h) * 2 + (i & 1)];
-    for (int i = tid; i < n_nodes; i += 128) sp[i] = parents[i];
+        cp_async16(sv + (size_t)(i >> 2) * 16 + (i & 3) * 4, qkv + (size_t)(i >> 2) * conv_ch + 2 * D.dn_k_heads * TV_DN + h * TV_DN + rb * 16 + (i & 3) * 4);
+    for (int i = tid; i < n_nodes * 2; i += 128) sg[i] = gate[((size_t)(i >> 1) * D.dn_v_heads + h) * 2 + (i & 1)];
+    for (int i = tid; i < n_nodes; i += 128) { sp[i] = parents[i]; ssrc[i] = src[i]; ssave[i] = save[i]; }
     cp_async_wait_all();
     __syncthreads();
+    const int rr = tid >> 3, sl = tid & 7;
+    const int vrow = rb * 16 + rr;
     float4 st[4];
     for (int t = 0; t < n_nodes; ++t) {
-        const int p = sp[t];
-        if (t == 0 || p != t - 1) {
-            if (p < 0) {
+        const int from = ssrc[t];
+        if (from != -2) {
+            const int p = sp[t];
+            if (from >= 0) {
 #pragma unroll
-                for (int r = 0; r < 4; ++r) st[r] = *(reinterpret_cast<const float4*>(ssm_state + (size_t)h * head_elems + (size_t)(v0 + r) * TV_DN) + lane);
+                for (int i = 0; i < 4; ++i) {
+                    const uint2 raw = slots[(from * 4 + i) * 128 + tid];
+                    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x)), b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+                    st[i] = make_float4(a.x, a.y, b.x, b.y);
+                }
+            } else if (p < 0 || p >= t) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) st[i] = *(reinterpret_cast<const float4*>(ssm_state + (size_t)h * head_elems + (size_t)vrow * TV_DN) + sl + 8 * i);
             } else {
                 uint2 raw[4];
 #pragma unroll
-                for (int r = 0; r < 4; ++r)
-                    raw[r] = *(reinterpret_cast<const uint2*>(node_states + ((size_t)p * D.dn_v_heads + h) * head_elems + (size_t)(v0 + r) * TV_DN) + lane);
+                for (int i = 0; i < 4; ++i)
+                    raw[i] = *(reinterpret_cast<const uint2*>(node_states + ((size_t)p * D.dn_v_heads + h) * head_elems + (size_t)vrow * TV_DN) + sl + 8 * i);
 #pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw[r].x)), b = __half22float2(*reinterpret_cast<const __half2*>(&raw[r].y));
-                    st[r] = make_float4(a.x, a.y, b.x, b.y);
+                for (int i = 0; i < 4; ++i) {
+                    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw[i].x)), b = __half22float2(*reinterpret_cast<const __half2*>(&raw[i].y));
+                    st[i] = make_float4(a.x, a.y, b.x, b.y);
                 }
             }
         }
-        const float4 q4 = *(reinterpret_cast<const float4*>(sq[t]) + lane);
-        const float4 k4 = *(reinterpret_cast<const float4*>(sk[t]) + lane);
-        const float beta = sg[t][0], decay = sg[t][1];
+        float4 q4[4], k4[4];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const float vv = sv[t][warp * 4 + r];
-            float4 u = st[r];
-            u.x = __fmul_rn(u.x, decay); u.y = __fmul_rn(u.y, decay); u.z = __fmul_rn(u.z, decay); u.w = __fmul_rn(u.w, decay);
-            float kv = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(u.x, k4.x), __fmul_rn(u.y, k4.y)), __fmul_rn(u.z, k4.z)), __fmul_rn(u.w, k4.w));
-            kv = warp_sum(kv);
-            const float delta = __fmul_rn(__fsub_rn(vv, kv), beta);
-            u.x = __fadd_rn(u.x, __fmul_rn(k4.x, delta)); u.y = __fadd_rn(u.y, __fmul_rn(k4.y, delta));
-            u.z = __fadd_rn(u.z, __fmul_rn(k4.z, delta)); u.w = __fadd_rn(u.w, __fmul_rn(k4.w, delta));
-            float o = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(u.x, q4.x), __fmul_rn(u.y, q4.y)), __fmul_rn(u.z, q4.z)), __fmul_rn(u.w, q4.w));
-            o = warp_sum(o);
-            st[r] = u;
-            const __half2 h0 = __floats2half2_rn(u.x, u.y), h1 = __floats2half2_rn(u.z, u.w);
-            *(reinterpret_cast<uint2*>(node_states + ((size_t)t * D.dn_v_heads + h) * head_elems + (size_t)(v0 + r) * TV_DN) + lane) =
-                make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
-            if (lane == 0) core[((size_t)t * D.dn_v_heads + h) * TV_DN + v0 + r] = o;
+        for (int i = 0; i < 4; ++i) {
+            q4[i] = *(reinterpret_cast<const float4*>(sq + (size_t)t * TV_DN) + sl + 8 * i);
+            k4[i] = *(reinterpret_cast<const float4*>(sk + (size_t)t * TV_DN) + sl + 8 * i);
         }
+        const float beta = sg[2 * t], decay = sg[2 * t + 1], vv = sv[t * 16 + rr];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            st[i].x = __fmul_rn(st[i].x, decay); st[i].y = __fmul_rn(st[i].y, decay); st[i].z = __fmul_rn(st[i].z, decay); st[i].w = __fmul_rn(st[i].w, decay);
+        }
+        float kv = __fadd_rn(__fadd_rn(dot4_rn(st[0], k4[0]), dot4_rn(st[1], k4[1])), __fadd_rn(dot4_rn(st[2], k4[2]), dot4_rn(st[3], k4[3])));
+        kv += __shfl_xor_sync(0xffffffffu, kv, 1); kv += __shfl_xor_sync(0xffffffffu, kv, 2); kv += __shfl_xor_sync(0xffffffffu, kv, 4);
+        const float delta = __fmul_rn(__fsub_rn(vv, kv), beta);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            st[i].x = __fadd_rn(st[i].x, __fmul_rn(k4[i].x, delta)); st[i].y = __fadd_rn(st[i].y, __fmul_rn(k4[i].y, delta));
+            st[i].z = __fadd_rn(st[i].z, __fmul_rn(k4[i].z, delta)); st[i].w = __fadd_rn(st[i].w, __fmul_rn(k4[i].w, delta));
+        }
+        float o = __fadd_rn(__fadd_rn(dot4_rn(st[0], q4[0]), dot4_rn(st[1], q4[1])), __fadd_rn(dot4_rn(st[2], q4[2]), dot4_rn(st[3], q4[3])));
+        o += __shfl_xor_sync(0xffffffffu, o, 1); o += __shfl_xor_sync(0xffffffffu, o, 2); o += __shfl_xor_sync(0xffffffffu, o, 4);
+        const int keep = ssave[t];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __half2 h0 = __floats2half2_rn(st[i].x, st[i].y), h1 = __floats2half2_rn(st[i].z, st[i].w);
+            const uint2 raw = make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+            *(reinterpret_cast<uint2*>(node_states + ((size_t)t * D.dn_v_heads + h) * head_elems + (size_t)vrow * TV_DN) + sl + 8 * i) = raw;
+            if (keep >= 0) slots[(keep * 4 + i) * 128 + tid] = raw;
+        }
+        if (sl == 0) core[((size_t)t * D.dn_v_heads + h) * TV_DN + vrow] = o;
     }
 }
 
@@ -570,7 +645,7 @@ __global__ void tv_commit_kv_kernel(bf16* __restrict__ k_cache, bf16* __restrict
 struct TvScratch {
     bf16 *hidden, *resid, *normed, *proj, *ba, *qbuf, *attn, *mlp, *logits;
     float *dn_qkv, *dn_gate, *core, *scores, *stats, *partial;
-    int* depth; unsigned long long* anc;
+    int* depth; unsigned long long* anc; int* dn_src; int* dn_save;
     size_t bytes;
 };
 
@@ -593,7 +668,7 @@ static TvScratch tv_layout(const TvDims& D, int n, int max_ctx, char* base) {
     s.core = (float*)take((size_t)n * D.dn_v_heads * TV_DN * 4);
     s.scores = (float*)take((size_t)n * D.q_heads * lpad * 4); s.stats = (float*)take((size_t)n * D.q_heads * 2 * 4);
     s.partial = (float*)take((size_t)n * D.q_heads * chunks * TV_HD * 4);
-    s.depth = (int*)take(64 * 4); s.anc = (unsigned long long*)take(64 * 8);
+    s.depth = (int*)take(64 * 4); s.anc = (unsigned long long*)take(64 * 8); s.dn_src = (int*)take(64 * 4); s.dn_save = (int*)take(64 * 4);
     s.bytes = off;
     return s;
 }
@@ -682,6 +757,7 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
     if (!attr_done) {
         Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
         Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_pv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        Q35_CUDA_OK(cudaFuncSetAttribute(tv_dn_tree_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tv_dn_tree_smem(TV_MAX_NODES)));
         attr_done = true;
     }
     const size_t kv_layer = (size_t)D.kv_heads * in->max_ctx * TV_HD;
@@ -689,7 +765,7 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
     const size_t nstate_layer = (size_t)in->max_nodes * state_layer, nconv_layer = (size_t)in->max_nodes * conv_ch;
     if (in->max_nodes < n) { set_error("tree_verify: max_nodes %d < n_nodes %d", in->max_nodes, n); return QWEN35_ERR_BAD_ARG; }
 
-    tv_tree_prep_kernel<<<1, 32, 0, stream>>>(in->parents, n, s.depth, s.anc);
+    tv_tree_prep_kernel<<<1, 32, 0, stream>>>(in->parents, n, s.depth, s.anc, s.dn_src, s.dn_save);
     if (in->dense_mask & 1u) tv_embed_dense_kernel<<<n, 256, 0, stream>>>((const bf16*)in->token_embd, in->node_tokens, D.hidden, s.hidden);
     else tv_embed_q4k_kernel<<<dim3(n, D.hidden / 256), 32, 0, stream>>>((const uint8_t*)in->token_embd, in->node_tokens, D.hidden, s.hidden);
     g_launches.fetch_add(2);
@@ -724,7 +800,7 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
             __half* nstates = (__half*)in->node_states + (size_t)i_dn * nstate_layer;
             tv_dn_conv_kernel<<<dim3(n, (conv_ch + 255) / 256), 256, 0, stream>>>(s.proj, dn_in, in->parents, cstate, (const float*)W.conv_w, conv_ch, s.dn_qkv, nconv);
             tv_dn_norm_kernel<<<dim3(n, D.dn_k_heads), 128, 0, stream>>>(s.dn_qkv, conv_ch, s.ba, 2 * D.dn_v_heads, (const float*)W.ssm_a, (const float*)W.dt_bias, D, s.dn_gate);
-            tv_dn_tree_kernel<<<dim3(D.dn_v_heads, TV_DN / 16), 128, 0, stream>>>(s.dn_qkv, conv_ch, s.dn_gate, in->parents, n, D,
+            tv_dn_tree_kernel<<<dim3(D.dn_v_heads, TV_DN / 16), 128, tv_dn_tree_smem(n), stream>>>(s.dn_qkv, conv_ch, s.dn_gate, in->parents, s.dn_src, s.dn_save, n, D,
                                                                                  (const float*)in->ssm_state + (size_t)i_dn * state_layer, nstates, s.core);
             tv_dn_gated_norm_kernel<<<dim3(n, D.dn_v_heads), 128, 0, stream>>>(s.core, s.proj, dn_in, z_off, (const float*)W.ssm_norm, D, s.attn);
             g_launches.fetch_add(4);
