@@ -344,10 +344,11 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
 // ------------------------------------------------------------------------------------------------------------
 // Q4_K weights: C[M <= 64, N] = epi(A[M, K] . dequant(W[N, K])^T).  Same split-K cluster scheme as above, but the
 // weight operand never exists in global memory as bf16:
-//   warp 0      TMA producer: activation tiles (two 64-wide slabs per 128-wide k-step) and RAW Q4_K super-blocks,
-//               one box of 144 bytes x 64 rows per half tile (a whole super-block row per request: HBM sees
-//               contiguous 144-byte pieces, never 16- or 32-byte ones)
-//   warps 2-9   dequantise from the raw ring into the 128-byte-swizzled bf16 tile the MMA descriptor expects:
+//   warp 0      TMA producer of the activation tiles (two 64-wide slabs per 128-wide k-step)
+//   warp 18     TMA producer of the RAW Q4_K super-blocks, one box of 144 bytes x 64 rows per half tile (a whole
+//               super-block row per request: HBM sees contiguous 144-byte pieces, never 16- or 32-byte ones); its own
+//               warp so that the raw ring runs its full depth ahead of the dequantisation
+//   warps 2-17  dequantise from the raw ring into the 128-byte-swizzled bf16 tile the MMA descriptor expects:
 //               a 64-weight group of a super-block is exactly one 64-wide slab row, so thread (row, h) converts
 //               group h of the k-step for one tile row (3 conflict-free 16-byte shared loads, 8 swizzled stores)
 //   warp 1      MMA issue: 8 x (M128 N128 K16) per k-step once both operands of the stage are there
@@ -360,8 +361,9 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
 // and bounded the kernel.  qwen35_b200_dequant_q4k keeps the published arithmetic bit for bit.  (An f16 weight
 // operand beside bf16 activations is not an option: kind::f16 with different A and B formats raised "illegal
 // instruction" on this GPU.)
-constexpr int Q4K_THREADS = 576;                                                      // 2 + 16 dequantisation warps
+constexpr int Q4K_THREADS = 608;                                                      // 2 + 16 dequantisation warps + the raw producer
 constexpr int Q4K_DQ_WARPS = 16;
+constexpr int Q4K_RAW_WARP = 2 + Q4K_DQ_WARPS;
 constexpr int Q4K_STAGES = 3, Q4K_RAW_STAGES = 3;
 constexpr uint32_t Q4K_A_SLAB = 64 * 128, Q4K_B_SLAB = 128 * 128;                      // bytes
 constexpr uint32_t Q4K_STAGE_BYTES = 2 * Q4K_A_SLAB + 2 * Q4K_B_SLAB;                 // 48 KB per 128-wide k-step
@@ -425,18 +427,10 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
+        // activation tiles: k-step i may be issued as soon as the MMAs of k-step i - STAGES have read the stage
         if (lane == 0) {
-            int issued_a = 0, issued_r = 0;
+            int issued_a = 0;
             for (int i = 0; i < nk2; ++i) {
-                if ((i & 1) == 0) {
-                    const int j = i >> 1, rs = j % RS;
-                    if (!g_mbar_wait(emptyr0 + 8 * rs, ((j / RS) & 1) ^ 1, p.err, s_abort)) break;
-                    g_mbar_expect_tx(fullr0 + 8 * rs, Q4K_RAW_BYTES);
-                    const uint32_t dst = rawring + rs * Q4K_RAW_BYTES;
-                    g_tma_load_2d(dst, &tmW, (sb_begin + j) * 144, n0, fullr0 + 8 * rs);
-                    g_tma_load_2d(dst + 64 * 144, &tmW, (sb_begin + j) * 144, (EPI == EPI_SILU_MUL ? p.up_row_offset : 64) + n0, fullr0 + 8 * rs);
-                    issued_r = j + 1;
-                }
                 const int st = i % STAGES;
                 if (!g_mbar_wait(empty0 + 8 * st, ((i / STAGES) & 1) ^ 1, p.err, s_abort)) break;
                 g_mbar_expect_tx(fulla0 + 8 * st, 2 * Q4K_A_SLAB);
@@ -451,6 +445,25 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
                     unsigned it = 0;
                     while (!g_mbar_try_wait(fulla0 + 8 * (i % STAGES), (i / STAGES) & 1) && ++it < GEMM_SPIN_LIMIT) {}
                 }
+            }
+        }
+    } else if (warp == Q4K_RAW_WARP) {
+        // raw super-blocks, a producer of their own: a slot is refilled the moment both k-steps of its super-block are
+        // dequantised, RS super-blocks ahead of the consumers, whatever the state of the activation ring (issued from the
+        // activation producer's loop, a refill waited for that loop's stage and ran barely one k-step ahead of its use)
+        if (lane == 0) {
+            int issued_r = 0;
+            const int nsb = sb_end - sb_begin;
+            for (int j = 0; j < nsb; ++j) {
+                const int rs = j % RS;
+                if (!g_mbar_wait(emptyr0 + 8 * rs, ((j / RS) & 1) ^ 1, p.err, s_abort)) break;
+                g_mbar_expect_tx(fullr0 + 8 * rs, Q4K_RAW_BYTES);
+                const uint32_t dst = rawring + rs * Q4K_RAW_BYTES;
+                g_tma_load_2d(dst, &tmW, (sb_begin + j) * 144, n0, fullr0 + 8 * rs);
+                g_tma_load_2d(dst + 64 * 144, &tmW, (sb_begin + j) * 144, (EPI == EPI_SILU_MUL ? p.up_row_offset : 64) + n0, fullr0 + 8 * rs);
+                issued_r = j + 1;
+            }
+            if (*s_abort) {
                 for (int j = max(0, issued_r - RS); j < issued_r; ++j) {
                     unsigned it = 0;
                     while (!g_mbar_try_wait(fullr0 + 8 * (j % RS), (j / RS) & 1) && ++it < GEMM_SPIN_LIMIT) {}

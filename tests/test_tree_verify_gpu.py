@@ -34,7 +34,8 @@ def test_q4k_dequant_gpu_bit_exact():
 
 
 @pytest.mark.parametrize("M,N,K,epi", [(33, 512, 512, 0), (7, 1000, 1024, 0), (40, 2048, 5120, 1), (33, 1024, 17408, 1), (33, 3584, 1024, 2),
-                                       (1, 128, 256, 0), (64, 640, 768, 2)])
+                                       (1, 128, 256, 0), (64, 640, 768, 2),
+                                       (33, 9472, 5120, 2)])     # 148 gate/up tiles of the 27B widths: one full wave, no split-K
 def test_q4k_gemm_matches_dequantised_reference(M, N, K, epi):
     """Fused dequantisation GEMM against torch on the oracle's bf16 weight operand: same values, f32 sums in a
     different order, so a few outputs may land one bf16 step away."""
