@@ -158,12 +158,47 @@ __device__ __forceinline__ float tv_block_sum(float v, float* red) {
 
 // y = bf16(x * rsqrt(mean x^2 + eps) * w), w f32 applied as a plain multiply (qwen35_target_graph.cpp:260-264)
 __global__ void __launch_bounds__(256) tv_rmsnorm_kernel(const bf16* __restrict__ x, const float* __restrict__ w, bf16* __restrict__ out, int H, float eps) {
+    // H is a multiple of 256; a thread keeps its (up to 4) 8-element pieces of the row in registers between the two passes
     __shared__ float red[8];
-    const bf16* xr = x + (size_t)blockIdx.x * H;
+    constexpr int MAXV = 4;
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)blockIdx.x * H);
+    const int nv = H / 8;
+    uint4 v[MAXV];
     float ss = 0.f;
-    for (int i = threadIdx.x; i < H; i += 256) { const float v = bf2f(xr[i]); ss = fmaf(v, v, ss); }
+#pragma unroll
+    for (int j = 0; j < MAXV; ++j) {
+        const int i = threadIdx.x + j * 256;
+        if (i < nv) {
+            v[j] = xr[i];
+            const bf16* e = reinterpret_cast<const bf16*>(&v[j]);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) { const float f = bf2f(e[k]); ss = fmaf(f, f, ss); }
+        }
+    }
+    for (int i = threadIdx.x + MAXV * 256; i < nv; i += 256) {          // rows wider than 8192: the tail is read twice
+        const uint4 t = xr[i];
+        const bf16* e = reinterpret_cast<const bf16*>(&t);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) { const float f = bf2f(e[k]); ss = fmaf(f, f, ss); }
+    }
     const float inv = rsqrt_ieee(tv_block_sum(ss, red) / (float)H + eps);
-    for (int i = threadIdx.x; i < H; i += 256) out[(size_t)blockIdx.x * H + i] = f2bf(bf2f(xr[i]) * inv * w[i]);
+    uint4* orow = reinterpret_cast<uint4*>(out + (size_t)blockIdx.x * H);
+    auto emit = [&](int i, const uint4& t) {
+        const bf16* e = reinterpret_cast<const bf16*>(&t);
+        const float4 w0 = *reinterpret_cast<const float4*>(w + (size_t)i * 8), w1 = *reinterpret_cast<const float4*>(w + (size_t)i * 8 + 4);
+        const float ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        uint4 o;
+        bf16* oe = reinterpret_cast<bf16*>(&o);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) oe[k] = f2bf(bf2f(e[k]) * inv * ws[k]);
+        orow[i] = o;
+    };
+#pragma unroll
+    for (int j = 0; j < MAXV; ++j) {
+        const int i = threadIdx.x + j * 256;
+        if (i < nv) emit(i, v[j]);
+    }
+    for (int i = threadIdx.x + MAXV * 256; i < nv; i += 256) emit(i, xr[i]);
 }
 
 // ------------------------------------------ full attention ------------------------------------------
@@ -386,14 +421,20 @@ __global__ void __launch_bounds__(128) tv_att_merge_kernel(const float* __restri
 }
 
 // --------------------------------------------- DeltaNet ---------------------------------------------
-// tree short-conv + SiLU: taps of node t = its three predecessors on the parent chain, continuing into the committed
-// conv state [3][channels] (row 2 newest) when the chain ends (qwen35_target_graph.cpp:462-496).  Also keeps the raw
-// projection row of every node for the commit.
-__global__ void __launch_bounds__(256) tv_dn_conv_kernel(const bf16* __restrict__ proj, int ldp, const int* __restrict__ parents,
-                                                         const float* __restrict__ conv_state, const float* __restrict__ conv_w, int conv_ch,
-                                                         float* __restrict__ qkv, float* __restrict__ node_conv) {
-    const int t = blockIdx.x, ch = blockIdx.y * 256 + threadIdx.x;
-    if (ch >= conv_ch) return;
+// tree short-conv + SiLU, then what the delta rule needs of it, in one kernel.  grid (nodes, conv channels / 128),
+// 128 threads: a block is one head-sized slice of the conv channels.
+//   conv: taps of node t = its three predecessors on the parent chain, continuing into the committed conv state
+//         [3][channels] (row 2 newest) when the chain ends (qwen35_target_graph.cpp:462-496); the raw projection row of
+//         every node is kept for the commit
+//   q and k slices: L2 norm of the head (q also scaled by 1/sqrt(128))
+//   v slice of head h: beta = sigmoid(b), decay = exp(softplus(a + dt_bias) * ssm_a) for (node, h)
+__global__ void __launch_bounds__(128) tv_dn_conv_norm_kernel(const bf16* __restrict__ proj, int ldp, const int* __restrict__ parents,
+                                                              const float* __restrict__ conv_state, const float* __restrict__ conv_w, int conv_ch,
+                                                              const bf16* __restrict__ ba, int ldba, const float* __restrict__ ssm_a,
+                                                              const float* __restrict__ dt_bias, TvDims D, float* __restrict__ qkv,
+                                                              float* __restrict__ node_conv, float* __restrict__ gate /* [nodes][v_heads][2] */) {
+    __shared__ float red[4];
+    const int t = blockIdx.x, hb = blockIdx.y, tid = threadIdx.x, ch = hb * TV_DN + tid;
     float x[4];
     x[3] = bf2f(proj[(size_t)t * ldp + ch]);
     node_conv[(size_t)t * conv_ch + ch] = x[3];
@@ -406,30 +447,20 @@ __global__ void __launch_bounds__(256) tv_dn_conv_kernel(const bf16* __restrict_
     const float4 w = *reinterpret_cast<const float4*>(conv_w + (size_t)ch * 4);
     float s = w.x * x[0];
     s = fmaf(w.y, x[1], s); s = fmaf(w.z, x[2], s); s = fmaf(w.w, x[3], s);
-    qkv[(size_t)t * conv_ch + ch] = silu_f(s);
-}
-
-// L2 norm of the q and k heads (q also scaled by 1/sqrt(128)), and per (node, v head): beta = sigmoid(b),
-// decay = exp(softplus(a + dt_bias) * ssm_a).  grid (nodes, k_heads), 128 threads
-__global__ void __launch_bounds__(128) tv_dn_norm_kernel(float* __restrict__ qkv, int conv_ch, const bf16* __restrict__ ba, int ldba,
-                                                         const float* __restrict__ ssm_a, const float* __restrict__ dt_bias, TvDims D,
-                                                         float* __restrict__ gate /* [nodes][v_heads][2] */) {
-    __shared__ float red[4];
-    const int t = blockIdx.x, kh = blockIdx.y, tid = threadIdx.x;
-    float* q = qkv + (size_t)t * conv_ch + kh * TV_DN;
-    float* k = q + D.dn_k_heads * TV_DN;
-    const float qv = q[tid], kv = k[tid];
-    const float qs = tv_block_sum(qv * qv, red);
-    const float ks = tv_block_sum(kv * kv, red);
-    q[tid] = qv * rsqrt_ieee(qs + D.eps) * 0.08838834764831845f;
-    k[tid] = kv * rsqrt_ieee(ks + D.eps);
-    for (int h = kh * 128 + tid; h < D.dn_v_heads; h += D.dn_k_heads * 128) {
+    float y = silu_f(s);
+    if (hb < 2 * D.dn_k_heads) {                              // block-uniform
+        const float ss = tv_block_sum(y * y, red);
+        y = y * rsqrt_ieee(ss + D.eps);
+        if (hb < D.dn_k_heads) y *= 0.08838834764831845f;
+    } else if (tid == 0) {
+        const int h = hb - 2 * D.dn_k_heads;
         const float b = bf2f(ba[(size_t)t * ldba + h]);
-        const float a = bf2f(ba[(size_t)t * ldba + D.dn_v_heads + h]) + dt_bias[h];
-        const float sp = (a > 20.f) ? a : log1pf(expf(a));
+        const float al = bf2f(ba[(size_t)t * ldba + D.dn_v_heads + h]) + dt_bias[h];
+        const float sp = (al > 20.f) ? al : log1pf(expf(al));
         gate[((size_t)t * D.dn_v_heads + h) * 2] = sigmoid_f(b);
         gate[((size_t)t * D.dn_v_heads + h) * 2 + 1] = expf(sp * ssm_a[h]);
     }
+    qkv[(size_t)t * conv_ch + ch] = y;
 }
 
 // tree gated delta rule: one CTA of 128 threads per (v head, block of 16 value rows); nodes in the given order.
@@ -760,6 +791,14 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
         Q35_CUDA_OK(cudaFuncSetAttribute(tv_dn_tree_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tv_dn_tree_smem(TV_MAX_NODES)));
         attr_done = true;
     }
+    // second stream for the work that runs beside a projection; made once for the process's device and forked from /
+    // joined into the caller's stream with events, so it is also legal inside a stream capture
+    static struct { cudaStream_t stream = nullptr; cudaEvent_t fork = nullptr, join = nullptr; } side;
+    if (!side.stream) {
+        Q35_CUDA_OK(cudaStreamCreateWithFlags(&side.stream, cudaStreamNonBlocking));
+        Q35_CUDA_OK(cudaEventCreateWithFlags(&side.fork, cudaEventDisableTiming));
+        Q35_CUDA_OK(cudaEventCreateWithFlags(&side.join, cudaEventDisableTiming));
+    }
     const size_t kv_layer = (size_t)D.kv_heads * in->max_ctx * TV_HD;
     const size_t state_layer = (size_t)D.dn_v_heads * TV_DN * TV_DN;
     const size_t nstate_layer = (size_t)in->max_nodes * state_layer, nconv_layer = (size_t)in->max_nodes * conv_ch;
@@ -793,17 +832,22 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
             att_w = D.q_heads * TV_HD;
             ++i_fa;
         } else {
+            // the small beta/alpha projection (a handful of CTAs) runs beside the input projection on a second stream
+            Q35_CUDA_OK(cudaEventRecord(side.fork, stream));
+            Q35_CUDA_OK(cudaStreamWaitEvent(side.stream, side.fork, 0));
+            Q35_TRYT(gemm_bf16(s.normed, D.hidden, (const bf16*)W.w_ba, 2 * D.dn_v_heads, s.ba, 2 * D.dn_v_heads, nullptr, 0, n, 2 * D.dn_v_heads, D.hidden, 0, 0, side.stream));
+            Q35_CUDA_OK(cudaEventRecord(side.join, side.stream));
             Q35_TRYT(q4k_linear(s.normed, D.hidden, W.w_in, (W.dense_mask & 1u) != 0, dn_in, D.hidden, s.proj, dn_in, nullptr, 0, n, 0, stream));
-            Q35_TRYT(gemm_bf16(s.normed, D.hidden, (const bf16*)W.w_ba, 2 * D.dn_v_heads, s.ba, 2 * D.dn_v_heads, nullptr, 0, n, 2 * D.dn_v_heads, D.hidden, 0, 0, stream));
             float* cstate = (float*)in->conv_state + (size_t)i_dn * 3 * conv_ch;
             float* nconv = (float*)in->node_conv + (size_t)i_dn * nconv_layer;
             __half* nstates = (__half*)in->node_states + (size_t)i_dn * nstate_layer;
-            tv_dn_conv_kernel<<<dim3(n, (conv_ch + 255) / 256), 256, 0, stream>>>(s.proj, dn_in, in->parents, cstate, (const float*)W.conv_w, conv_ch, s.dn_qkv, nconv);
-            tv_dn_norm_kernel<<<dim3(n, D.dn_k_heads), 128, 0, stream>>>(s.dn_qkv, conv_ch, s.ba, 2 * D.dn_v_heads, (const float*)W.ssm_a, (const float*)W.dt_bias, D, s.dn_gate);
+            Q35_CUDA_OK(cudaStreamWaitEvent(stream, side.join, 0));
+            tv_dn_conv_norm_kernel<<<dim3(n, conv_ch / TV_DN), 128, 0, stream>>>(s.proj, dn_in, in->parents, cstate, (const float*)W.conv_w, conv_ch, s.ba, 2 * D.dn_v_heads,
+                                                                              (const float*)W.ssm_a, (const float*)W.dt_bias, D, s.dn_qkv, nconv, s.dn_gate);
             tv_dn_tree_kernel<<<dim3(D.dn_v_heads, TV_DN / 16), 128, tv_dn_tree_smem(n), stream>>>(s.dn_qkv, conv_ch, s.dn_gate, in->parents, s.dn_src, s.dn_save, n, D,
                                                                                  (const float*)in->ssm_state + (size_t)i_dn * state_layer, nstates, s.core);
             tv_dn_gated_norm_kernel<<<dim3(n, D.dn_v_heads), 128, 0, stream>>>(s.core, s.proj, dn_in, z_off, (const float*)W.ssm_norm, D, s.attn);
-            g_launches.fetch_add(4);
+            g_launches.fetch_add(3);
             att_w = D.dn_v_heads * TV_DN;
             ++i_dn;
         }
