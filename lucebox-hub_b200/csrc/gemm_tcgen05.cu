@@ -168,10 +168,11 @@ template <int EPI>
 __device__ __forceinline__ void cluster_reduce_store(const GemmParams& p, uint32_t park_local, int S, int rows, int m0, int n0, int t, int nt) {
     constexpr int BN_OUT = (EPI == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
     const uint32_t rank = cluster_ctarank();
-    const int slice = BN_OUT / S;                       // a multiple of 8
-    for (int item = t; item < rows * (slice / 8); item += nt) {
+    // 8-column groups rank, rank + S, rank + 2S, ... of the tile belong to this CTA (any S up to the group count)
+    const int my_groups = (BN_OUT / 8 - (int)rank + S - 1) / S;
+    for (int item = t; item < rows * my_groups; item += nt) {
         const int r = item % rows, cg = item / rows;
-        const int col = (int)rank * slice + cg * 8;     // first of 8 output columns within the tile
+        const int col = ((int)rank + cg * S) * 8;       // first of 8 output columns within the tile
         float g[8], u[8], v[GEMM_MAX_SPLIT][8];
 #pragma unroll
         for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
@@ -763,8 +764,19 @@ int gemm_q4k(const bf16* A, int lda, const uint8_t* W, int w_rows, bf16* C, int 
     GemmParams qp{M, N, K, C, ldc, R, ldr, up_row_offset, (int*)ws};
     const int bn_out = (epi == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
     const int n_tiles = (N + bn_out - 1) / bn_out, nsb = K / 256;
-    int split = 1;
-    while (split < GEMM_MAX_SPLIT && n_tiles * split < 120 && nsb / (split * 2) >= 2) split *= 2;      // >= 2 super-blocks per CTA
+    // one CTA per SM: the largest split (cluster size, not necessarily a power of two) that keeps the whole grid in ONE
+    // wave, with at least 2 super-blocks per CTA.  (Doubling until "about full" put 40-tile shapes at 160 CTAs: a second
+    // wave for 12 of them doubled the time.)
+    static int sm_count = 0;
+    if (!sm_count) {
+        int dev = 0;
+        Q35_CUDA_OK(cudaGetDevice(&dev));
+        Q35_CUDA_OK(cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev));
+    }
+    int split = sm_count / n_tiles;
+    if (split > GEMM_MAX_SPLIT) split = GEMM_MAX_SPLIT;
+    if (split < 1) split = 1;
+    while (split > 1 && nsb / split < 2) --split;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(n_tiles, 1, split);
     cfg.blockDim = dim3(Q4K_THREADS);
