@@ -196,6 +196,42 @@ def tree_verify_bench(dev, n_nodes=33, ctx=4096, iters=5):
             "roofline_frac": alg / (ms * 1e-3) / 1e9 / measured_peak()[0], "tflops": flops / (ms * 1e-3) / 1e12}
 
 
+def draft_forward_bench(dev, ctx=2048, iters=8):
+    """Draft side of the speculative loop: the 5-layer DFlash draft at the reference's widths (hidden 5120, 32 / 8 heads of
+    128, FFN 17408), bf16 random-init weights, a 2048-position feature window (the reference's cap) and 16 noise rows:
+    milliseconds per forward with CUDA events.  Bytes: all draft weights once + the feature window; flops: 2 x weights x
+    rows they multiply."""
+    from qwen35_b200.dflash_draft import DFLASH_27B as D, DraftModel, make_random_draft_weights
+    w = make_random_draft_weights(D, 5, device=dev)
+    m = DraftModel(D, w, max_ctx=ctx, device=dev)
+    g = torch.Generator(device=dev).manual_seed(5)
+    noise = torch.randn(D.q_len, D.hidden, device=dev, generator=g).bfloat16()
+    thc = torch.randn(ctx, D.n_target_layers * D.hidden, device=dev, generator=g).bfloat16()
+    lib = m._lib
+    times = []
+    l0 = lib.qwen35_b200_launch_count()
+    for i in range(3 + iters):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        m.forward(noise, thc)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        if i >= 3:
+            times.append(e0.elapsed_time(e1))
+    m.check_status()
+    launches = (lib.qwen35_b200_launch_count() - l0) // (3 + iters)
+    ms = min(times)
+    T = ctx + D.q_len
+    fc_p = D.hidden * D.n_target_layers * D.hidden
+    per_layer_q = D.q_dim * D.hidden * 2 + 3 * D.inter * D.hidden            # wq, wo, gate, up, down: 16 rows each
+    per_layer_kv = 2 * D.kv_dim * D.hidden                                    # wkv: all T rows
+    alg = 2.0 * (fc_p + D.n_layers * (per_layer_q + per_layer_kv)) + 2.0 * ctx * D.n_target_layers * D.hidden
+    flops = 2.0 * (fc_p * ctx + D.n_layers * (per_layer_q * D.q_len + per_layer_kv * T)) + D.n_layers * 4.0 * D.q_len * D.n_heads * D.head_dim * T
+    return {"workload": "DFlash draft forward: 5 layers, hidden 5120, bf16, %d-position feature window + 16 noise rows" % ctx,
+            "ms_per_forward": ms, "launches_per_forward": int(launches), "algorithmic_bytes": alg, "hbm_gbs": alg / (ms * 1e-3) / 1e9,
+            "hbm_frac": alg / (ms * 1e-3) / 1e9 / measured_peak()[0], "tflops": flops / (ms * 1e-3) / 1e12}
+
+
 def batched_decode_bench(weights_gpu, dev, rank, n_seq, ctx, n_steps, kernel_table=False, groups=1):
     """Batched-decode configuration: `n_seq` independent sequences per GPU, `ctx`-token contexts prefilled by the library's own
     prefill, `n_steps` greedy steps.  Returns (tok/s on this rank, ms per step, algorithmic bytes per step)."""
@@ -420,9 +456,10 @@ def run_ours(args):
     sweep = None
     if args.prefill_sweep and rank == 0:
         sweep = prefill_sweep(wg, dev, [int(x) for x in args.prefill_sweep.split(",")])
-    tree = None
+    tree = draft = None
     if args.tree_verify and rank == 0:
         tree = tree_verify_bench(dev)
+        draft = draft_forward_bench(dev)
     batched = None
     if args.batched > 0:
         b_tok_s, b_ms, b_bytes = batched_decode_bench(wg, dev, rank, args.batched, args.batched_ctx, GEN, kernel_table=args.kernel_table and rank == 0, groups=args.batched_groups)
@@ -483,6 +520,8 @@ def run_ours(args):
             line["prefill_sweep"] = sweep
         if tree:
             line["tree_verify"] = tree
+        if draft is not None:
+            line["draft_forward"] = draft
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(w_cpu, ids_cpu, 16, use_hf=False)
             if batched:

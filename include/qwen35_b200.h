@@ -277,6 +277,13 @@ typedef struct {
     void* scratch; size_t scratch_bytes;   /* caller-owned, >= qwen35_b200_tree_scratch_bytes() */
     const void* dbg_teacher;         /* optional bf16 [n_layers][n_nodes][hidden]: layer l > 0 reads row block l as its input */
     unsigned int dense_mask;         /* bit 0: token_embd is plain bf16 [vocab][hidden]; bit 1: output_w is */
+    /* Feature capture for the draft (qwen35_target_graph.cpp:743-787): when target_feat is given, the output of layer
+     * capture_layers[k] for node t is written to row (past + t) % feat_cap, columns [k*hidden, (k+1)*hidden) of the
+     * ring; tree_commit moves the accepted nodes' rows to positions past, past+1, ... (test_dflash.cpp:1455-1480). */
+    void* target_feat;               /* optional bf16 [feat_cap][n_capture * hidden] */
+    int feat_cap;                    /* ring capacity in positions */
+    int n_capture;                   /* 0..8 captured layers */
+    int capture_layers[8];           /* layer indices, ascending (the reference's target: 1, 16, 31, 46, 61) */
 } Qwen35TreeVerifyArgs;
 
 size_t qwen35_b200_tree_scratch_bytes(const Qwen35TreeDims* dims, int n_nodes, int max_ctx);
@@ -305,6 +312,54 @@ int qwen35_b200_draft_topk(const float* logits, int n_positions, int vocab, int 
  * token / parent arrays are what qwen35_b200_tree_verify takes (after the caller puts the root token in slot 0). */
 int qwen35_b200_build_ddtree(const float* top_log_probs, const int* top_token_ids, int depth_max, int k, int budget, int chain_seed,
                              int* token_ids, int* depths, int* parents, unsigned char* visibility);
+
+/* DFlash draft forward: the 5-layer non-causal block-diffusion draft that proposes q_len tokens from the target's captured
+ * features (build_draft_graph, models/qwen35_27b/src/qwen3_dflash_graph.cpp:38-166; weights DraftWeights / DraftLayer,
+ * src/internal.h).  Stateless like the reference (no KV cache): every call projects the whole feature window.
+ *   target_feat = rms_norm(fc . target_hidden_cat) * hidden_norm                       [ctx_len][hidden]
+ *   per layer:  Q = wq . norm(h) (per-head RMSNorm, NEOX RoPE at ctx_len + i);  K, V = wk, wv . [target_feat ; norm(h)]
+ *               (K per-head RMSNorm, NEOX RoPE at 0 .. ctx_len + q_len - 1);  non-causal attention over all keys, scale
+ *               1/sqrt(head_dim);  h += wo . attn;  h += w_down . (silu(w_gate . norm(h)) * (w_up . norm(h)))
+ *   hidden_out = rms_norm(h) * out_norm;  optional logits = lm_head . hidden_out (the target's head, bf16 or Q4_K)
+ * All matrices are bf16 [out][in] on the device; wkv is the row concatenation [wk ; wv], w_gate_up is [w_gate ; w_up];
+ * norm weights are f32 and multiply plainly.  head_dim must be 128, q_len * (n_heads / n_kv_heads) <= 64, hidden and
+ * inter multiples of 256.  Every module output is rounded once to bf16 (the reference keeps f32 activations between
+ * ggml ops; bf16 storage is this build's convention on every path). */
+typedef struct Qwen35DraftDims {
+    int hidden, n_layers, n_heads, n_kv_heads, head_dim, inter, n_target_layers, q_len;
+    float eps, rope_theta;
+} Qwen35DraftDims;
+typedef struct Qwen35DraftLayer {
+    const void* attn_norm;   /* f32 [hidden] */
+    const void* wq;          /* bf16 [n_heads * head_dim][hidden] */
+    const void* wkv;         /* bf16 [2 * n_kv_heads * head_dim][hidden]: k rows, then v rows */
+    const void* q_norm;      /* f32 [head_dim] */
+    const void* k_norm;      /* f32 [head_dim] */
+    const void* wo;          /* bf16 [hidden][n_heads * head_dim] */
+    const void* ffn_norm;    /* f32 [hidden] */
+    const void* w_gate_up;   /* bf16 [2 * inter][hidden]: gate rows, then up rows */
+    const void* w_down;      /* bf16 [hidden][inter] */
+} Qwen35DraftLayer;
+typedef struct Qwen35DraftArgs {
+    Qwen35DraftDims dims;
+    const Qwen35DraftLayer* layers;      /* HOST array [n_layers] of device pointers */
+    const void* fc;                      /* bf16 [hidden][n_target_layers * hidden] */
+    const void* hidden_norm;             /* f32 [hidden] */
+    const void* out_norm;                /* f32 [hidden] */
+    const void* noise_embed;             /* bf16 [q_len][hidden]: the target's embedding of [last token, MASK x (q_len-1)] */
+    const void* target_hidden_cat;       /* bf16 [ctx_len][n_target_layers * hidden] */
+    int ctx_len;                         /* >= 0 */
+    void* hidden_out;                    /* bf16 [q_len][hidden] */
+    const void* lm_head;                 /* optional: [vocab][hidden] bf16, or Q4_K super-blocks when lm_head_q4k != 0 */
+    int lm_head_q4k;
+    int vocab;
+    void* logits_out;                    /* bf16 [q_len][vocab] when lm_head is given */
+    void* scratch;                       /* device, >= qwen35_b200_draft_scratch_bytes(dims, ctx_len) */
+    size_t scratch_bytes;
+    qwen35_stream_t stream;
+} Qwen35DraftArgs;
+size_t qwen35_b200_draft_scratch_bytes(const Qwen35DraftDims* dims, int max_ctx_len);
+int qwen35_b200_draft_forward(const Qwen35DraftArgs* args);
 
 /* The prefill and batched-decode entry points keep a host copy of the device pointer tables, keyed by the two
  * table addresses, exactly as the reference keeps its host copy (prefill.cu:1179-1195): after the first call they

@@ -19,6 +19,7 @@
 #include <cmath>
 
 #include "common.cuh"
+#include "norm_kernels.cuh"
 #include "runtime.h"
 
 namespace q35 {
@@ -142,63 +143,6 @@ __global__ void tv_tree_prep_kernel(const int* __restrict__ parents, int n, int*
             for (int i = 0; i < TV_DN_SLOTS && keep < 0; ++i) if (owner[i] < 0) { owner[i] = t; keep = i; }
         save[t] = keep;
     }
-}
-
-// ---------------------------------------------- norms ----------------------------------------------
-__device__ __forceinline__ float tv_block_sum(float v, float* red) {
-    v = warp_sum(v);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float t = 0.f;
-    for (int i = 0; i < nw; ++i) t += red[i];
-    return t;
-}
-
-// y = bf16(x * rsqrt(mean x^2 + eps) * w), w f32 applied as a plain multiply (qwen35_target_graph.cpp:260-264)
-__global__ void __launch_bounds__(256) tv_rmsnorm_kernel(const bf16* __restrict__ x, const float* __restrict__ w, bf16* __restrict__ out, int H, float eps) {
-    // H is a multiple of 256; a thread keeps its (up to 4) 8-element pieces of the row in registers between the two passes
-    __shared__ float red[8];
-    constexpr int MAXV = 4;
-    const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)blockIdx.x * H);
-    const int nv = H / 8;
-    uint4 v[MAXV];
-    float ss = 0.f;
-#pragma unroll
-    for (int j = 0; j < MAXV; ++j) {
-        const int i = threadIdx.x + j * 256;
-        if (i < nv) {
-            v[j] = xr[i];
-            const bf16* e = reinterpret_cast<const bf16*>(&v[j]);
-#pragma unroll
-            for (int k = 0; k < 8; ++k) { const float f = bf2f(e[k]); ss = fmaf(f, f, ss); }
-        }
-    }
-    for (int i = threadIdx.x + MAXV * 256; i < nv; i += 256) {          // rows wider than 8192: the tail is read twice
-        const uint4 t = xr[i];
-        const bf16* e = reinterpret_cast<const bf16*>(&t);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) { const float f = bf2f(e[k]); ss = fmaf(f, f, ss); }
-    }
-    const float inv = rsqrt_ieee(tv_block_sum(ss, red) / (float)H + eps);
-    uint4* orow = reinterpret_cast<uint4*>(out + (size_t)blockIdx.x * H);
-    auto emit = [&](int i, const uint4& t) {
-        const bf16* e = reinterpret_cast<const bf16*>(&t);
-        const float4 w0 = *reinterpret_cast<const float4*>(w + (size_t)i * 8), w1 = *reinterpret_cast<const float4*>(w + (size_t)i * 8 + 4);
-        const float ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        uint4 o;
-        bf16* oe = reinterpret_cast<bf16*>(&o);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) oe[k] = f2bf(bf2f(e[k]) * inv * ws[k]);
-        orow[i] = o;
-    };
-#pragma unroll
-    for (int j = 0; j < MAXV; ++j) {
-        const int i = threadIdx.x + j * 256;
-        if (i < nv) emit(i, v[j]);
-    }
-    for (int i = threadIdx.x + MAXV * 256; i < nv; i += 256) emit(i, xr[i]);
 }
 
 // ------------------------------------------ full attention ------------------------------------------
@@ -672,6 +616,27 @@ __global__ void tv_commit_kv_kernel(bf16* __restrict__ k_cache, bf16* __restrict
     }
 }
 
+// feature capture: rows of `hidden` (node t) -> ring row (past + t) % cap, column block k.  grid nodes, 256 threads
+__global__ void __launch_bounds__(256) tv_capture_kernel(const bf16* __restrict__ hidden, int H, int past, int cap, int row_elems, int col0,
+                                                         bf16* __restrict__ ring) {
+    const int t = blockIdx.x;
+    const uint4* src = reinterpret_cast<const uint4*>(hidden + (size_t)t * H);
+    uint4* dst = reinterpret_cast<uint4*>(ring + (size_t)((past + t) % cap) * row_elems + col0);
+    for (int i = threadIdx.x; i < H / 8; i += 256) dst[i] = src[i];
+}
+// ring rows of the accepted nodes move to positions past, past+1, ... (ascending, so no source is overwritten early;
+// path[d] >= d because node numbers grow along a path)
+__global__ void tv_commit_feat_kernel(bf16* __restrict__ ring, int row_elems, int cap, int past, const int* __restrict__ path, const int* __restrict__ result) {
+    const int len = result[0];
+    for (int d = 0; d < len; ++d) {
+        const int src = (past + path[d]) % cap, dst = (past + d) % cap;
+        if (src == dst) continue;
+        const uint4* s = reinterpret_cast<const uint4*>(ring + (size_t)src * row_elems);
+        uint4* o = reinterpret_cast<uint4*>(ring + (size_t)dst * row_elems);
+        for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < row_elems / 8; i += gridDim.x * blockDim.x) o[i] = s[i];
+    }
+}
+
 // ------------------------------------------------ host ------------------------------------------------
 struct TvScratch {
     bf16 *hidden, *resid, *normed, *proj, *ba, *qbuf, *attn, *mlp, *logits;
@@ -803,6 +768,10 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
     const size_t state_layer = (size_t)D.dn_v_heads * TV_DN * TV_DN;
     const size_t nstate_layer = (size_t)in->max_nodes * state_layer, nconv_layer = (size_t)in->max_nodes * conv_ch;
     if (in->max_nodes < n) { set_error("tree_verify: max_nodes %d < n_nodes %d", in->max_nodes, n); return QWEN35_ERR_BAD_ARG; }
+    if (in->target_feat && (in->feat_cap < n || in->n_capture < 1 || in->n_capture > 8)) {
+        set_error("tree_verify: feature ring needs feat_cap >= n_nodes and 1..8 capture layers");
+        return QWEN35_ERR_BAD_ARG;
+    }
 
     tv_tree_prep_kernel<<<1, 32, 0, stream>>>(in->parents, n, s.depth, s.anc, s.dn_src, s.dn_save);
     if (in->dense_mask & 1u) tv_embed_dense_kernel<<<n, 256, 0, stream>>>((const bf16*)in->token_embd, in->node_tokens, D.hidden, s.hidden);
@@ -858,6 +827,12 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
         Q35_TRYT(q4k_linear(s.mlp, D.ffn, W.w_down, (W.dense_mask & 8u) != 0, D.hidden, D.ffn, s.hidden, D.hidden, s.resid, D.hidden, n, 1, stream));
         if (in->dbg_hidden)
             Q35_CUDA_OK(cudaMemcpyAsync((bf16*)in->dbg_hidden + (size_t)il * n * D.hidden, s.hidden, (size_t)n * D.hidden * 2, cudaMemcpyDeviceToDevice, stream));
+        if (in->target_feat)
+            for (int k = 0; k < in->n_capture; ++k)
+                if (in->capture_layers[k] == il) {
+                    tv_capture_kernel<<<n, 256, 0, stream>>>(s.hidden, D.hidden, in->past, in->feat_cap, in->n_capture * D.hidden, k * D.hidden, (bf16*)in->target_feat);
+                    g_launches.fetch_add(1);
+                }
     }
     tv_rmsnorm_kernel<<<n, 256, 0, stream>>>(s.hidden, (const float*)in->output_norm, s.normed, D.hidden, D.eps);
     Q35_TRYT(q4k_linear(s.normed, D.hidden, in->output_w, (in->dense_mask & 2u) != 0, D.vocab, D.hidden, s.logits, D.vocab, nullptr, 0, n, 0, stream));
@@ -896,6 +871,10 @@ extern "C" int qwen35_b200_tree_commit(const Qwen35TreeVerifyArgs* in, const int
     if (n_fa > 0)
         tv_commit_kv_kernel<<<(n_fa * D.kv_heads * (TV_HD / 8) * 2 + 255) / 256, 256, 0, stream>>>((bf16*)in->k_cache, (bf16*)in->v_cache, (size_t)D.kv_heads * in->max_ctx * TV_HD,
                                                                                                  n_fa, D.kv_heads, in->max_ctx, in->past, path, result);
+    if (in->target_feat && in->n_capture > 0 && in->feat_cap > 0) {
+        tv_commit_feat_kernel<<<8, 256, 0, stream>>>((bf16*)in->target_feat, in->n_capture * D.hidden, in->feat_cap, in->past, path, result);
+        g_launches.fetch_add(1);
+    }
     Q35_CUDA_OK(cudaGetLastError());
     g_launches.fetch_add(3);
     return QWEN35_OK;

@@ -77,6 +77,25 @@ class TreeVerifyArgs(C.Structure):
         ("k_cache", C.c_void_p), ("v_cache", C.c_void_p), ("ssm_state", C.c_void_p), ("conv_state", C.c_void_p), ("node_states", C.c_void_p),
         ("node_conv", C.c_void_p), ("node_argmax", C.c_void_p), ("logits_out", C.c_void_p), ("dbg_hidden", C.c_void_p), ("dbg_num_layers", C.c_int),
         ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t), ("dbg_teacher", C.c_void_p), ("dense_mask", C.c_uint),
+        ("target_feat", C.c_void_p), ("feat_cap", C.c_int), ("n_capture", C.c_int), ("capture_layers", C.c_int * 8),
+    ]
+
+
+class DraftDimsC(C.Structure):
+    _fields_ = [(k, C.c_int) for k in ("hidden", "n_layers", "n_heads", "n_kv_heads", "head_dim", "inter", "n_target_layers", "q_len")] + \
+               [("eps", C.c_float), ("rope_theta", C.c_float)]
+
+
+class DraftLayerC(C.Structure):
+    _fields_ = [(k, C.c_void_p) for k in ("attn_norm", "wq", "wkv", "q_norm", "k_norm", "wo", "ffn_norm", "w_gate_up", "w_down")]
+
+
+class DraftArgs(C.Structure):
+    _fields_ = [
+        ("dims", DraftDimsC), ("layers", C.POINTER(DraftLayerC)), ("fc", C.c_void_p), ("hidden_norm", C.c_void_p), ("out_norm", C.c_void_p),
+        ("noise_embed", C.c_void_p), ("target_hidden_cat", C.c_void_p), ("ctx_len", C.c_int), ("hidden_out", C.c_void_p), ("lm_head", C.c_void_p),
+        ("lm_head_q4k", C.c_int), ("vocab", C.c_int), ("logits_out", C.c_void_p), ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t),
+        ("stream", C.c_void_p),
     ]
 
 
@@ -101,6 +120,8 @@ SIGNATURES = {
     "qwen35_b200_forget_tables": (None, []),
     "qwen35_b200_draft_topk": (_i, [_vp, _i, _i, _i, C.c_float, _vp, _vp, _vp]),
     "qwen35_b200_build_ddtree": (_i, [_vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
+    "qwen35_b200_draft_scratch_bytes": (C.c_size_t, [C.POINTER(DraftDimsC), _i]),
+    "qwen35_b200_draft_forward": (_i, [C.POINTER(DraftArgs)]),
     "qwen35_b200_tree_scratch_bytes": (C.c_size_t, [C.POINTER(TreeDimsC), _i, _i]),
     "qwen35_b200_tree_verify": (_i, [C.POINTER(TreeVerifyArgs), _vp]),
     "qwen35_b200_tree_accept": (_i, [_vp, _vp, _vp, _i, _vp, _vp, _vp]),

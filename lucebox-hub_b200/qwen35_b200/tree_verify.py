@@ -126,7 +126,9 @@ def random_tree(n_nodes, max_depth, seed):
 class TreeTarget:
     """Caches, weights table and scratch of one target model instance on one GPU."""
 
-    def __init__(self, dims: TreeDims, weights, max_ctx: int, device="cuda", max_nodes: int = MAX_NODES):
+    def __init__(self, dims: TreeDims, weights, max_ctx: int, device="cuda", max_nodes: int = MAX_NODES, capture_layers=(), feat_cap: int = 0):
+        """capture_layers / feat_cap: keep the outputs of those layers in a ring of feat_cap positions for the draft
+        (`target_feat`, bf16 [feat_cap, len(capture_layers) * hidden]; the reference's target captures layers 1, 16, 31, 46, 61)."""
         self.dims, self.max_ctx, self.max_nodes = dims, int(max_ctx), int(max_nodes)
         self.device = torch.device(device)
         self._lib = _capi.lib()
@@ -162,6 +164,12 @@ class TreeTarget:
         self.past = 0
         self._tokens = self._parents = None
         self._n = 0
+        self.capture_layers = tuple(int(x) for x in capture_layers)
+        if len(self.capture_layers) > 8:
+            raise ValueError("at most 8 capture layers")
+        self.feat_cap = int(feat_cap) if self.capture_layers else 0
+        self.target_feat = (torch.zeros(self.feat_cap, len(self.capture_layers) * D.hidden, dtype=torch.bfloat16, device=dev)
+                            if self.feat_cap > 0 else None)
 
     def _args(self, n, **kw):
         a = _capi.TreeVerifyArgs()
@@ -178,6 +186,10 @@ class TreeTarget:
         a.node_argmax = self.node_argmax.data_ptr()
         a.scratch = self._scratch.data_ptr(); a.scratch_bytes = self._scratch.numel()
         a.dense_mask = self._dense_mask
+        if self.target_feat is not None:
+            a.target_feat = self.target_feat.data_ptr(); a.feat_cap = self.feat_cap; a.n_capture = len(self.capture_layers)
+            for i, il in enumerate(self.capture_layers):
+                a.capture_layers[i] = il
         for k, v in kw.items():
             setattr(a, k, _capi.ptr(v) if torch.is_tensor(v) else v)
         return a
@@ -211,6 +223,15 @@ class TreeTarget:
         n_acc = int(result[0].item())
         self.past += n_acc
         return n_acc
+
+    def feature_window(self, n_last: int):
+        """The last `n_last` committed positions of the feature ring in position order, bf16 [n, n_capture * hidden]:
+        what the draft takes as target_hidden_cat (test_dflash.cpp:1097-1120 copies the same window out of the ring)."""
+        if self.target_feat is None:
+            raise ValueError("no feature ring: construct with capture_layers and feat_cap")
+        n = min(int(n_last), self.past, self.feat_cap)
+        idx = (torch.arange(self.past - n, self.past, device=self.device) % self.feat_cap)
+        return self.target_feat.index_select(0, idx)
 
     def check_status(self):
         _capi.check(self._lib.qwen35_b200_status(None), "status")

