@@ -155,16 +155,22 @@ def prefill_sweep(weights_gpu, dev, lengths):
     return out
 
 
-def tree_verify_bench(dev, n_nodes=33, ctx=4096, iters=5):
+def tree_verify_bench(dev, n_nodes=33, ctx=4096, iters=5, kv_type="bf16"):
     """Tree-verify configuration: 27B-class dims, Q4_K weights generated directly as random super-blocks (dequantised
     sigma ~0.02), a 4096-token context of random cache contents, one 33-node tree (seeded random parents, depth <= 8):
     milliseconds per verify + accept walk + commit, timed with CUDA events."""
     from qwen35_b200.tree_verify import QWEN35_27B as T, TreeTarget, make_random_tree_weights, random_tree
     w = make_random_tree_weights(T, 11, device=dev)
-    tt = TreeTarget(T, w, max_ctx=ctx + 128, device=dev)
+    tt = TreeTarget(T, w, max_ctx=ctx + 128, device=dev, kv_type=kv_type)
     g = torch.Generator(device=dev).manual_seed(11)
-    tt.k_cache.copy_(torch.randn(tt.k_cache.shape, device=dev, generator=g).bfloat16())
-    tt.v_cache.copy_(torch.randn(tt.v_cache.shape, device=dev, generator=g).bfloat16())
+    if kv_type == "q8_0":            # random Q8_0 rows: f16 d = 1/127 (bytes 0x08, 0x20), int8 values uniform
+        for c in (tt.k_cache, tt.v_cache):
+            blocks = c.view(-1, 34)
+            blocks.copy_(torch.randint(0, 256, blocks.shape, device=dev, generator=g, dtype=torch.uint8))
+            blocks[:, 0] = 0x08; blocks[:, 1] = 0x20
+    else:
+        tt.k_cache.copy_(torch.randn(tt.k_cache.shape, device=dev, generator=g).bfloat16())
+        tt.v_cache.copy_(torch.randn(tt.v_cache.shape, device=dev, generator=g).bfloat16())
     tt.ssm_state.copy_(0.01 * torch.randn(tt.ssm_state.shape, device=dev, generator=g))
     tt.conv_state.copy_(0.1 * torch.randn(tt.conv_state.shape, device=dev, generator=g))
     parents = torch.tensor(random_tree(n_nodes, 8, 11), dtype=torch.int32, device=dev)
@@ -187,11 +193,11 @@ def tree_verify_bench(dev, n_nodes=33, ctx=4096, iters=5):
     launches = (lib.qwen35_b200_launch_count() - l0) // (3 + iters)
     ms = min(times)
     w_bytes = (24_352_522_240 + 1_271_398_400) * 0.5625
-    kv_bytes = T.n_fa * T.kv_heads * (ctx + n_nodes) * T.head_dim * 2 * 2
+    kv_bytes = T.n_fa * T.kv_heads * (ctx + n_nodes) * (T.head_dim * 2 if kv_type == "bf16" else T.head_dim // 32 * 34) * 2
     st_bytes = T.n_dn * n_nodes * T.dn_v_heads * T.dn_dim * T.dn_dim * 2
     alg = w_bytes + kv_bytes + st_bytes
     flops = 2 * (24_352_522_240 + 1_271_398_400) * n_nodes
-    return {"workload": "tree verify: 27B-class dims (64 layers, hidden 5120), Q4_K weights, %d-token context, %d-node tree" % (ctx, n_nodes),
+    return {"workload": "tree verify: 27B-class dims (64 layers, hidden 5120), Q4_K weights, %s K/V cache, %d-token context, %d-node tree" % (kv_type, ctx, n_nodes),
             "ms_per_verify_commit": ms, "accepted": acc, "launches_per_pass": int(launches), "algorithmic_bytes": alg, "hbm_gbs": alg / (ms * 1e-3) / 1e9,
             "roofline_frac": alg / (ms * 1e-3) / 1e9 / measured_peak()[0], "tflops": flops / (ms * 1e-3) / 1e12}
 
@@ -459,6 +465,8 @@ def run_ours(args):
     tree = draft = None
     if args.tree_verify and rank == 0:
         tree = tree_verify_bench(dev)
+        tree["q8_0_kv_cache_ms"] = tree_verify_bench(dev, iters=3, kv_type="q8_0")["ms_per_verify_commit"]
+        torch.cuda.empty_cache()
         draft = draft_forward_bench(dev)
     batched = None
     if args.batched > 0:

@@ -145,12 +145,72 @@ __global__ void tv_tree_prep_kernel(const int* __restrict__ parents, int n, int*
     }
 }
 
+// K / V cache rows: bf16 [256] (512 bytes), or Q8_0 (the reference's default cache type, qwen35_target_graph.cpp:110-122):
+// 8 blocks of {f16 d, 32 x int8} = 272 bytes, quantised from the f32 values when a row is written
+// (d = amax / 127, q = roundf(x / d)) and read back as the bf16 operand bf16(d * q).
+constexpr int TV_Q8_ROW = (TV_HD / 32) * 34;
+__host__ __device__ constexpr int tv_kv_row_bytes(int kv_type) { return kv_type ? TV_Q8_ROW : TV_HD * 2; }
+
+// one warp = one 32-element block: lane holds element `lane` of the block
+__device__ __forceinline__ void tv_q8_store_block(unsigned char* blk, float v, int lane) {
+    const float amax = warp_max(fabsf(v));
+    const float d = amax / 127.0f;
+    const float id = d != 0.f ? 1.0f / d : 0.f;
+    blk[2 + lane] = (unsigned char)(signed char)(int)roundf(v * id);
+    if (lane == 0) *reinterpret_cast<__half*>(blk) = __float2half_rn(d);
+}
+
+// stage 128 cache rows [j0, j0 + 128) of one kv head into the padded bf16 tile; rows >= L are zero.  bf16 rows are copied
+// straight into the tile; Q8_0 rows are copied raw into `raw` and converted by tv_finish_rows after the copies landed.
+template <bool Q8>
+__device__ __forceinline__ void tv_stage_rows(bf16* tile, unsigned char* raw, const unsigned char* head_base, int j0, int L, int tid) {
+    if (Q8) {
+        for (int i = tid; i < TV_CHUNK * (TV_Q8_ROW / 16); i += 256) {
+            const int k = i / (TV_Q8_ROW / 16), c = i % (TV_Q8_ROW / 16);
+            if (j0 + k < L) cp_async16(raw + (size_t)k * TV_Q8_ROW + c * 16, head_base + (size_t)(j0 + k) * TV_Q8_ROW + c * 16);
+        }
+    } else {
+        for (int i = tid; i < TV_CHUNK * (TV_HD / 8); i += 256) {
+            const int k = i / (TV_HD / 8), c8 = i % (TV_HD / 8);
+            bf16* dst = tile + (size_t)k * TV_QSTRIDE + c8 * 8;
+            if (j0 + k < L) cp_async16(dst, head_base + ((size_t)(j0 + k) * TV_HD + c8 * 8) * 2);
+            else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+        }
+    }
+}
+// call after cp_async_wait_all() + __syncthreads(); for Q8_0 converts the raw rows and synchronises again
+template <bool Q8>
+__device__ __forceinline__ void tv_finish_rows(bf16* tile, const unsigned char* raw, int j0, int L, int tid) {
+    if (!Q8) return;
+    for (int i = tid; i < TV_CHUNK * (TV_HD / 32); i += 256) {
+        const int k = i / (TV_HD / 32), b = i % (TV_HD / 32);
+        uint32_t o[16];
+        if (j0 + k < L) {
+            const unsigned char* blk = raw + (size_t)k * TV_Q8_ROW + b * 34;
+            const float d = __half2float(*reinterpret_cast<const __half*>(blk));
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+                const unsigned short two = *reinterpret_cast<const unsigned short*>(blk + 2 + 2 * e);
+                const __nv_bfloat162 pr = __floats2bfloat162_rn(d * (float)(signed char)(two & 0xFF), d * (float)(signed char)(two >> 8));
+                o[e] = *reinterpret_cast<const uint32_t*>(&pr);
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) o[e] = 0u;
+        }
+        uint4* dst = reinterpret_cast<uint4*>(tile + (size_t)k * TV_QSTRIDE + b * 32);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) dst[e] = make_uint4(o[4 * e], o[4 * e + 1], o[4 * e + 2], o[4 * e + 3]);
+    }
+    __syncthreads();
+}
+
 // ------------------------------------------ full attention ------------------------------------------
 // one CTA (128 threads, 2 elements each) per (node, slot): q heads, then k heads, then v heads of the projection row
 // [per q head: q(256) | gate(256)] [k heads] [v heads].  Head RMSNorm (plain weight), rotate-half RoPE over rot_dim.
 __global__ void __launch_bounds__(128) tv_fa_prep_kernel(const bf16* __restrict__ proj, int ldp, const float* __restrict__ qn, const float* __restrict__ kn,
                                                          const int* __restrict__ depth, TvDims D, int past, int max_ctx,
-                                                         bf16* __restrict__ qbuf, bf16* __restrict__ k_cache, bf16* __restrict__ v_cache) {
+                                                         bf16* __restrict__ qbuf, unsigned char* __restrict__ k_cache, unsigned char* __restrict__ v_cache, int kv_type) {
     __shared__ float red[4];
     __shared__ float xs[TV_HD];
     const int t = blockIdx.x, slot = blockIdx.y, tid = threadIdx.x;
@@ -159,8 +219,14 @@ __global__ void __launch_bounds__(128) tv_fa_prep_kernel(const bf16* __restrict_
     if (slot >= D.q_heads + D.kv_heads) {                      // v head: copy into the cache slot
         const int kvh = slot - D.q_heads - D.kv_heads;
         const bf16* src = row + qcols + (D.kv_heads + kvh) * TV_HD;
-        bf16* dst = v_cache + ((size_t)kvh * max_ctx + past + t) * TV_HD;
-        dst[tid] = src[tid]; dst[tid + 128] = src[tid + 128];
+        unsigned char* vrow = v_cache + ((size_t)kvh * max_ctx + past + t) * tv_kv_row_bytes(kv_type);
+        if (kv_type) {                                             // warp w holds blocks w and 4 + w
+            tv_q8_store_block(vrow + (tid >> 5) * 34, bf2f(src[tid]), tid & 31);
+            tv_q8_store_block(vrow + (4 + (tid >> 5)) * 34, bf2f(src[tid + 128]), tid & 31);
+        } else {
+            bf16* dst = reinterpret_cast<bf16*>(vrow);
+            dst[tid] = src[tid]; dst[tid + 128] = src[tid + 128];
+        }
         return;
     }
     const bool isq = slot < D.q_heads;
@@ -187,14 +253,21 @@ __global__ void __launch_bounds__(128) tv_fa_prep_kernel(const bf16* __restrict_
         }
         y[k] = v;
     }
+    if (!isq && kv_type) {
+        unsigned char* krow = k_cache + ((size_t)(slot - D.q_heads) * max_ctx + past + t) * TV_Q8_ROW;
+        tv_q8_store_block(krow + (tid >> 5) * 34, y[0], tid & 31);
+        tv_q8_store_block(krow + (4 + (tid >> 5)) * 34, y[1], tid & 31);
+        return;
+    }
     bf16* dst = isq ? qbuf + ((size_t)t * D.q_heads + slot) * TV_HD
-                    : k_cache + ((size_t)(slot - D.q_heads) * max_ctx + past + t) * TV_HD;
+                    : reinterpret_cast<bf16*>(k_cache + ((size_t)(slot - D.q_heads) * max_ctx + past + t) * TV_HD * 2);
     dst[tid] = f2bf(y[0]); dst[tid + 128] = f2bf(y[1]);
 }
 
 // scores of all query rows of one kv head (row r = node * gqa + q-in-group) against one chunk of keys:
 // s = (q . k) / 16 in f32, masked to -inf outside [0, past) and the node's ancestors.  grid (chunks, kv_heads).
-__global__ void __launch_bounds__(256, 1) tv_att_scores_kernel(const bf16* __restrict__ qbuf, const bf16* __restrict__ k_cache,
+template <bool Q8>
+__global__ void __launch_bounds__(256, 1) tv_att_scores_kernel(const bf16* __restrict__ qbuf, const unsigned char* __restrict__ k_cache,
                                                                const unsigned long long* __restrict__ anc, TvDims D, int n_nodes, int past,
                                                                int max_ctx, int lpad, float* __restrict__ scores) {
     extern __shared__ __align__(16) unsigned char tv_smem[];
@@ -210,14 +283,11 @@ __global__ void __launch_bounds__(256, 1) tv_att_scores_kernel(const bf16* __res
         if (r < R) cp_async16(dst, qbuf + ((size_t)(r / gqa) * D.q_heads + kvh * gqa + r % gqa) * TV_HD + c8 * 8);
         else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
     }
-    for (int i = tid; i < TV_CHUNK * (TV_HD / 8); i += 256) {
-        const int k = i / (TV_HD / 8), c8 = i % (TV_HD / 8);
-        bf16* dst = Ks + (size_t)k * TV_QSTRIDE + c8 * 8;
-        if (j0 + k < L) cp_async16(dst, k_cache + ((size_t)kvh * max_ctx + j0 + k) * TV_HD + c8 * 8);
-        else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
-    }
+    unsigned char* raw = reinterpret_cast<unsigned char*>(Ks + (size_t)TV_CHUNK * TV_QSTRIDE);      // Q8_0 only
+    tv_stage_rows<Q8>(Ks, raw, k_cache + (size_t)kvh * max_ctx * tv_kv_row_bytes(Q8), j0, L, tid);
     cp_async_wait_all();
     __syncthreads();
+    tv_finish_rows<Q8>(Ks, raw, j0, L, tid);
     const int g = lane >> 2, c = lane & 3;
     for (int nt = warp; nt < TV_CHUNK / 8; nt += 8) {
         uint32_t bfr[TV_HD / 16][2];
@@ -285,7 +355,8 @@ __global__ void __launch_bounds__(256) tv_att_stats_kernel(const float* __restri
 // partial P.V of one chunk of keys for all query rows of one kv head; P = bf16(exp(s - m) / l).  grid (chunks, kv_heads).
 // The V chunk is staged row-major by cp.async and read as the B operand with ldmatrix.trans; P goes to shared memory
 // row-major and is read as the A operand with ldmatrix.
-__global__ void __launch_bounds__(256, 1) tv_att_pv_kernel(const bf16* __restrict__ v_cache, const float* __restrict__ scores, const float* __restrict__ stats,
+template <bool Q8>
+__global__ void __launch_bounds__(256, 1) tv_att_pv_kernel(const unsigned char* __restrict__ v_cache, const float* __restrict__ scores, const float* __restrict__ stats,
                                                            TvDims D, int n_nodes, int past, int max_ctx, int lpad, float* __restrict__ partial) {
     extern __shared__ __align__(16) unsigned char tv_smem[];
     bf16* Vs = reinterpret_cast<bf16*>(tv_smem);                     // [TV_CHUNK keys][TV_QSTRIDE]
@@ -293,12 +364,8 @@ __global__ void __launch_bounds__(256, 1) tv_att_pv_kernel(const bf16* __restric
     const int gqa = D.q_heads / D.kv_heads, R = n_nodes * gqa, mt_n = (R + 15) / 16;
     const int chunk = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int j0 = chunk * TV_CHUNK, L = past + n_nodes;
-    for (int i = tid; i < TV_CHUNK * (TV_HD / 8); i += 256) {
-        const int k = i / (TV_HD / 8), c8 = i % (TV_HD / 8);
-        bf16* dst = Vs + (size_t)k * TV_QSTRIDE + c8 * 8;
-        if (j0 + k < L) cp_async16(dst, v_cache + ((size_t)kvh * max_ctx + j0 + k) * TV_HD + c8 * 8);
-        else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
-    }
+    unsigned char* raw = reinterpret_cast<unsigned char*>(Ps + (size_t)mt_n * 16 * TV_PSTRIDE);      // Q8_0 only
+    tv_stage_rows<Q8>(Vs, raw, v_cache + (size_t)kvh * max_ctx * tv_kv_row_bytes(Q8), j0, L, tid);
     // P rows (overlapping the copies above): a warp takes one row at a time, a lane four consecutive keys, so the score
     // loads are 16-byte, coalesced and several rows deep in flight
     static_assert(TV_CHUNK == 128, "one warp covers a 128-key row with four keys per lane");
@@ -318,6 +385,7 @@ __global__ void __launch_bounds__(256, 1) tv_att_pv_kernel(const bf16* __restric
     }
     cp_async_wait_all();
     __syncthreads();
+    tv_finish_rows<Q8>(Vs, raw, j0, L, tid);
     const int g = lane >> 2, c = lane & 3;
     const int n_chunks = gridDim.x;
     for (int np = warp; np < TV_HD / 16; np += 8) {                   // pairs of 8-dim output tiles
@@ -597,21 +665,22 @@ __global__ void tv_commit_conv_kernel(const float* __restrict__ node_conv, size_
         cs[ch] = nv[0]; cs[conv_ch + ch] = nv[1]; cs[2 * (size_t)conv_ch + ch] = nv[2];
     }
 }
-// K/V rows of the accepted nodes move to slots past, past+1, ... (ascending, so no source is overwritten early)
-__global__ void tv_commit_kv_kernel(bf16* __restrict__ k_cache, bf16* __restrict__ v_cache, size_t layer_stride, int n_fa, int kv_heads, int max_ctx, int past,
-                                    const int* __restrict__ path, const int* __restrict__ result) {
+// K/V rows of the accepted nodes move to slots past, past+1, ... (ascending, so no source is overwritten early).
+// Rows are row_bytes long (512 bf16, 272 Q8_0), copied in 16-byte pieces.
+__global__ void tv_commit_kv_kernel(unsigned char* __restrict__ k_cache, unsigned char* __restrict__ v_cache, size_t layer_stride, int n_fa, int kv_heads,
+                                    int max_ctx, int row_bytes, int past, const int* __restrict__ path, const int* __restrict__ result) {
     const int len = result[0];
-    const int per_row = TV_HD / 8;
+    const int per_row = row_bytes / 16;
     const size_t total = (size_t)n_fa * kv_heads * per_row * 2;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-        const int c8 = (int)(i % per_row);
+        const int c16 = (int)(i % per_row);
         const size_t rest = i / per_row;
         const int which = (int)(rest % 2);
         const size_t lh = rest / 2;                  // layer * kv_heads + head
-        bf16* base = (which ? v_cache : k_cache) + (lh / kv_heads) * layer_stride + ((lh % kv_heads) * (size_t)max_ctx) * TV_HD + c8 * 8;
+        unsigned char* base = (which ? v_cache : k_cache) + (lh / kv_heads) * layer_stride + ((lh % kv_heads) * (size_t)max_ctx) * row_bytes + c16 * 16;
         for (int d = 0; d < len; ++d) {
             const int src = past + path[d], dst = past + d;
-            if (src != dst) *reinterpret_cast<uint4*>(base + (size_t)dst * TV_HD) = *reinterpret_cast<const uint4*>(base + (size_t)src * TV_HD);
+            if (src != dst) *reinterpret_cast<uint4*>(base + (size_t)dst * row_bytes) = *reinterpret_cast<const uint4*>(base + (size_t)src * row_bytes);
         }
     }
 }
@@ -751,8 +820,10 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
     const size_t pv_smem = ((size_t)TV_CHUNK * TV_QSTRIDE + (size_t)mt_n * 16 * TV_PSTRIDE) * 2;
     static bool attr_done = false;
     if (!attr_done) {
-        Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-        Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_pv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_scores_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_scores_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_pv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_pv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
         Q35_CUDA_OK(cudaFuncSetAttribute(tv_dn_tree_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tv_dn_tree_smem(TV_MAX_NODES)));
         attr_done = true;
     }
@@ -764,7 +835,9 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
         Q35_CUDA_OK(cudaEventCreateWithFlags(&side.fork, cudaEventDisableTiming));
         Q35_CUDA_OK(cudaEventCreateWithFlags(&side.join, cudaEventDisableTiming));
     }
-    const size_t kv_layer = (size_t)D.kv_heads * in->max_ctx * TV_HD;
+    const bool q8 = in->kv_type != 0;
+    const size_t kv_layer = (size_t)D.kv_heads * in->max_ctx * tv_kv_row_bytes(in->kv_type);      // bytes
+    const size_t q8_raw = q8 ? (size_t)TV_CHUNK * TV_Q8_ROW : 0;
     const size_t state_layer = (size_t)D.dn_v_heads * TV_DN * TV_DN;
     const size_t nstate_layer = (size_t)in->max_nodes * state_layer, nconv_layer = (size_t)in->max_nodes * conv_ch;
     if (in->max_nodes < n) { set_error("tree_verify: max_nodes %d < n_nodes %d", in->max_nodes, n); return QWEN35_ERR_BAD_ARG; }
@@ -789,13 +862,15 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
         int att_w;
         if (is_fa) {
             Q35_TRYT(q4k_linear(s.normed, D.hidden, W.w_in, (W.dense_mask & 1u) != 0, fa_in, D.hidden, s.proj, fa_in, nullptr, 0, n, 0, stream));
-            bf16* kc = (bf16*)in->k_cache + (size_t)i_fa * kv_layer;
-            bf16* vc = (bf16*)in->v_cache + (size_t)i_fa * kv_layer;
+            unsigned char* kc = (unsigned char*)in->k_cache + (size_t)i_fa * kv_layer;
+            unsigned char* vc = (unsigned char*)in->v_cache + (size_t)i_fa * kv_layer;
             tv_fa_prep_kernel<<<dim3(n, D.q_heads + 2 * D.kv_heads), 128, 0, stream>>>(s.proj, fa_in, (const float*)W.q_norm, (const float*)W.k_norm, s.depth, D,
-                                                                                       in->past, in->max_ctx, s.qbuf, kc, vc);
-            tv_att_scores_kernel<<<dim3(chunks, D.kv_heads), 256, sc_smem, stream>>>(s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores);
+                                                                                       in->past, in->max_ctx, s.qbuf, kc, vc, in->kv_type);
+            if (q8) tv_att_scores_kernel<true><<<dim3(chunks, D.kv_heads), 256, sc_smem + q8_raw, stream>>>(s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores);
+            else tv_att_scores_kernel<false><<<dim3(chunks, D.kv_heads), 256, sc_smem, stream>>>(s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores);
             tv_att_stats_kernel<<<(D.kv_heads * R + 7) / 8, 256, 0, stream>>>(s.scores, D.kv_heads * R, lpad, chunks * TV_CHUNK, s.stats);
-            tv_att_pv_kernel<<<dim3(chunks, D.kv_heads), 256, pv_smem, stream>>>(vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial);
+            if (q8) tv_att_pv_kernel<true><<<dim3(chunks, D.kv_heads), 256, pv_smem + q8_raw, stream>>>(vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial);
+            else tv_att_pv_kernel<false><<<dim3(chunks, D.kv_heads), 256, pv_smem, stream>>>(vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial);
             tv_att_merge_kernel<<<dim3(n, D.q_heads), 128, 0, stream>>>(s.partial, s.proj, fa_in, D, n, chunks, s.attn);
             g_launches.fetch_add(5);
             att_w = D.q_heads * TV_HD;
@@ -869,8 +944,9 @@ extern "C" int qwen35_b200_tree_commit(const Qwen35TreeVerifyArgs* in, const int
         tv_commit_conv_kernel<<<148, 256, 0, stream>>>((const float*)in->node_conv, (size_t)in->max_nodes * conv_ch, conv_ch, n_dn, path, result, (float*)in->conv_state);
     }
     if (n_fa > 0)
-        tv_commit_kv_kernel<<<(n_fa * D.kv_heads * (TV_HD / 8) * 2 + 255) / 256, 256, 0, stream>>>((bf16*)in->k_cache, (bf16*)in->v_cache, (size_t)D.kv_heads * in->max_ctx * TV_HD,
-                                                                                                 n_fa, D.kv_heads, in->max_ctx, in->past, path, result);
+        tv_commit_kv_kernel<<<(n_fa * D.kv_heads * (TV_HD / 8) * 2 + 255) / 256, 256, 0, stream>>>((unsigned char*)in->k_cache, (unsigned char*)in->v_cache,
+                                                                                                 (size_t)D.kv_heads * in->max_ctx * tv_kv_row_bytes(in->kv_type), n_fa, D.kv_heads,
+                                                                                                 in->max_ctx, tv_kv_row_bytes(in->kv_type), in->past, path, result);
     if (in->target_feat && in->n_capture > 0 && in->feat_cap > 0) {
         tv_commit_feat_kernel<<<8, 256, 0, stream>>>((bf16*)in->target_feat, in->n_capture * D.hidden, in->feat_cap, in->past, path, result);
         g_launches.fetch_add(1);

@@ -77,7 +77,7 @@ class TreeVerifyArgs(C.Structure):
         ("k_cache", C.c_void_p), ("v_cache", C.c_void_p), ("ssm_state", C.c_void_p), ("conv_state", C.c_void_p), ("node_states", C.c_void_p),
         ("node_conv", C.c_void_p), ("node_argmax", C.c_void_p), ("logits_out", C.c_void_p), ("dbg_hidden", C.c_void_p), ("dbg_num_layers", C.c_int),
         ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t), ("dbg_teacher", C.c_void_p), ("dense_mask", C.c_uint),
-        ("target_feat", C.c_void_p), ("feat_cap", C.c_int), ("n_capture", C.c_int), ("capture_layers", C.c_int * 8),
+        ("target_feat", C.c_void_p), ("feat_cap", C.c_int), ("n_capture", C.c_int), ("capture_layers", C.c_int * 8), ("kv_type", C.c_int),
     ]
 
 

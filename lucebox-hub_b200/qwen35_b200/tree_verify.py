@@ -126,8 +126,11 @@ def random_tree(n_nodes, max_depth, seed):
 class TreeTarget:
     """Caches, weights table and scratch of one target model instance on one GPU."""
 
-    def __init__(self, dims: TreeDims, weights, max_ctx: int, device="cuda", max_nodes: int = MAX_NODES, capture_layers=(), feat_cap: int = 0):
-        """capture_layers / feat_cap: keep the outputs of those layers in a ring of feat_cap positions for the draft
+    def __init__(self, dims: TreeDims, weights, max_ctx: int, device="cuda", max_nodes: int = MAX_NODES, capture_layers=(), feat_cap: int = 0,
+                 kv_type: str = "bf16"):
+        """kv_type: "bf16" or "q8_0" (the reference's default K / V cache type): Q8_0 caches are uint8
+        [n_fa, kv_heads, max_ctx, 272], rows quantised in the kernel when a node is written.
+        capture_layers / feat_cap: keep the outputs of those layers in a ring of feat_cap positions for the draft
         (`target_feat`, bf16 [feat_cap, len(capture_layers) * hidden]; the reference's target captures layers 1, 16, 31, 46, 61)."""
         self.dims, self.max_ctx, self.max_nodes = dims, int(max_ctx), int(max_nodes)
         self.device = torch.device(device)
@@ -150,7 +153,13 @@ class TreeTarget:
             self._layers_c[il].dense_mask = mask
         self._dense_mask = (1 if weights["token_embd"].dtype == torch.bfloat16 else 0) | (2 if weights["output_w"].dtype == torch.bfloat16 else 0)
         dev = self.device
-        self.k_cache = torch.zeros(max(D.n_fa, 1), D.kv_heads, self.max_ctx, D.head_dim, dtype=torch.bfloat16, device=dev)
+        if kv_type not in ("bf16", "q8_0"):
+            raise ValueError("kv_type must be 'bf16' or 'q8_0'")
+        self.kv_type = kv_type
+        if kv_type == "q8_0":
+            self.k_cache = torch.zeros(max(D.n_fa, 1), D.kv_heads, self.max_ctx, D.head_dim // 32 * 34, dtype=torch.uint8, device=dev)
+        else:
+            self.k_cache = torch.zeros(max(D.n_fa, 1), D.kv_heads, self.max_ctx, D.head_dim, dtype=torch.bfloat16, device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
         self.ssm_state = torch.zeros(max(D.n_dn, 1), D.dn_v_heads, D.dn_dim, D.dn_dim, dtype=torch.float32, device=dev)
         self.conv_state = torch.zeros(max(D.n_dn, 1), 3, D.conv_ch, dtype=torch.float32, device=dev)
@@ -186,6 +195,7 @@ class TreeTarget:
         a.node_argmax = self.node_argmax.data_ptr()
         a.scratch = self._scratch.data_ptr(); a.scratch_bytes = self._scratch.numel()
         a.dense_mask = self._dense_mask
+        a.kv_type = 1 if self.kv_type == "q8_0" else 0
         if self.target_feat is not None:
             a.target_feat = self.target_feat.data_ptr(); a.feat_cap = self.feat_cap; a.n_capture = len(self.capture_layers)
             for i, il in enumerate(self.capture_layers):

@@ -86,14 +86,48 @@ def q4k_gemm_operand(blocks: np.ndarray) -> np.ndarray:
     return out
 
 
+def q8_0_quant(x: np.ndarray) -> np.ndarray:
+    """Q8_0 packing of f32 rows [..., 32k] -> uint8 [..., 34k]: per 32 elements f16 d = amax / 127 then 32 int8
+    q = round-half-away(x * (1 / d)) with the UNROUNDED f32 d (d = 0 -> all zero), as ggml's quantize_row_q8_0 and
+    gguf-py's Q8_0.quantize_blocks do.  Pinned bit for bit to gguf-py 0.19.0 (tests/golden/q8_0_golden.npz)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    blk = x.reshape(-1, 32)
+    d = np.abs(blk).max(axis=1, keepdims=True) / np.float32(127)
+    with np.errstate(divide="ignore"):
+        inv = np.where(d == 0, np.float32(0), np.float32(1) / d).astype(np.float32)
+    y = blk * inv
+    q = (np.sign(y) * np.floor(np.abs(y) + np.float32(0.5))).astype(np.int8)        # roundf: halves away from zero
+    out = np.empty((blk.shape[0], 34), np.uint8)
+    out[:, :2] = d.astype(np.float16).view(np.uint8).reshape(-1, 2)
+    out[:, 2:] = q.view(np.uint8)
+    return out.reshape(*x.shape[:-1], x.shape[-1] // 32 * 34)
+
+
+def q8_0_dequant(b: np.ndarray) -> np.ndarray:
+    """uint8 [..., 34k] -> f32 [..., 32k]: d (f16 -> f32) * q."""
+    blk = np.ascontiguousarray(b, dtype=np.uint8).reshape(-1, 34)
+    d = blk[:, :2].copy().view(np.float16).astype(np.float32)
+    q = blk[:, 2:].copy().view(np.int8).astype(np.float32)
+    return (d * q).reshape(*b.shape[:-1], b.shape[-1] // 34 * 32)
+
+
+def q8_0_cache_value(x: torch.Tensor) -> torch.Tensor:
+    """What a Q8_0 cache row written from f32 values x holds: d * q, exact in f32 (11 + 7 significant bits), so that
+    quantising it again gives back the same bytes.  The attention reads it as the bf16 operand bf16(d * q): the oracle
+    applies that rounding where it uses K and V."""
+    return torch.from_numpy(q8_0_dequant(q8_0_quant(x.numpy())))
+
+
 def rb(x: torch.Tensor) -> torch.Tensor:
     return x.bfloat16().float()
 
 
 class TreeOracle:
-    def __init__(self, dims, weights, max_ctx):
-        """weights: the dict of qwen35_b200.tree_verify.make_random_tree_weights on the CPU."""
-        self.D, self.max_ctx = dims, max_ctx
+    def __init__(self, dims, weights, max_ctx, kv_q8=False):
+        """weights: the dict of qwen35_b200.tree_verify.make_random_tree_weights on the CPU.  kv_q8: the K / V cache is
+        Q8_0 (the reference's default, qwen35_target_graph.cpp:110-122): rows are quantised from their f32 values when
+        written and read back as bf16(d * q)."""
+        self.D, self.max_ctx, self.kv_q8 = dims, max_ctx, bool(kv_q8)
         D = dims
 
         def mat(blocks):
@@ -152,15 +186,20 @@ class TreeOracle:
                 vv = proj[2 * D.q_heads * 256 + D.kv_heads * 256:].reshape(D.kv_heads, 256)
                 hn = lambda t, w: t * torch.rsqrt((t * t).mean(-1, keepdim=True) + D.rms_eps) * w      # noqa: E731
                 q = rb(self._rope(hn(q, W["q_norm"]), pos))
-                kk = rb(self._rope(hn(kk, W["k_norm"]), pos))
+                kk = self._rope(hn(kk, W["k_norm"]), pos)
+                if self.kv_q8:
+                    kk, vv = q8_0_cache_value(kk), q8_0_cache_value(vv)
+                else:
+                    kk = rb(kk)
                 K = torch.cat([ctx["k"][i_fa], kk[:, None]], 1); V = torch.cat([ctx["v"][i_fa], vv[:, None]], 1)
                 new["k"].append(K); new["v"].append(V)
                 gqa = D.q_heads // D.kv_heads
                 out = torch.zeros(D.q_heads, 256)
+                Kb, Vb = rb(K), rb(V)                        # the tensor-core operands (identity for a bf16 cache)
                 for h in range(D.q_heads):
-                    s = (K[h // gqa] @ q[h]) * 0.0625
+                    s = (Kb[h // gqa] @ q[h]) * 0.0625
                     p = torch.exp(s - s.max()); p = rb(p / p.sum())
-                    out[h] = p @ V[h // gqa]
+                    out[h] = p @ Vb[h // gqa]
                 att = rb(out * torch.sigmoid(gate)).reshape(-1)
                 i_fa += 1
             else:

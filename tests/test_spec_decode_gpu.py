@@ -62,29 +62,63 @@ def test_spec_loop_reproduces_sequential_greedy(budget, prompt_len):
     print(f"budget {budget}: {same}/{n_gen} tokens equal the sequential greedy run; rounds {sd.stats['steps']}, "
           f"committed {sd.stats['committed']}, mean tree {sd.stats['tree_nodes'] / sd.stats['steps']:.1f} nodes")
     assert same >= 2
-    # a draft that knows the continuation: several tokens are accepted per round and the output stays the greedy one
-    if same == n_gen:
-        sd2 = SpecDecoder(target(), wg, D, dw, mask_token_id=T.vocab - 1, budget=budget)
-        out2 = [sd2.prefill(prompt)]
-        real_forward = sd2.draft.forward
 
-        def knowing_forward(noise, window):
-            hidden, logits = real_forward(noise, window)          # the real kernels still run; only the proposal is replaced
-            logits = torch.full_like(logits, -4.0)
-            for j in range(1, D.q_len):
-                idx = len(out2) + j - 1
-                logits[j, ref[idx] if idx < n_gen else 0] = 8.0
-            return hidden, logits
-        sd2.draft.forward = knowing_forward
-        while len(out2) < n_gen:
-            out2.extend(sd2.step())
-        sd2.target.check_status()
-        agree = sum(1 for a, b in zip(out2[:n_gen], ref) if a == b)
-        print(f"  with a knowing draft: {sd2.stats['steps']} rounds for {n_gen} tokens, {sd2.stats['committed'] / sd2.stats['steps']:.1f} committed per round, "
-              f"{agree}/{n_gen} tokens equal")
-        assert sd2.stats["steps"] < sd.stats["steps"] and sd2.stats["committed"] / sd2.stats["steps"] >= 2.0
-        first_diff = next((i for i in range(n_gen) if out2[i] != ref[i]), n_gen)
-        assert first_diff == n_gen or gaps[first_diff - 1] <= 2 * LOGIT_NOISE
+
+def test_spec_loop_accepts_deep_paths_from_a_knowing_draft():
+    """Several tokens per round: the proposal is replaced by the target's own greedy look-ahead (computed on a second
+    target instance kept in lockstep, snapshot / restore around the look-ahead), so whole chains are accepted and
+    committed.  Every emitted token must be the lockstep target's arg-max given the same prefix, or within the bf16 noise
+    of it (deep tree nodes see their keys in other cache slots than a sequential run: another f32 summation order; with
+    random weights the two best logits are often that close)."""
+    budget, prompt_len, n_gen = 32, 20, 40
+    T, wg, D, dw, target, SpecDecoder = _build(77, budget)
+    prompt = np.random.default_rng(3).integers(0, T.vocab, prompt_len)
+    sd = SpecDecoder(target(), wg, D, dw, mask_token_id=T.vocab - 1, budget=budget)
+    look = target()
+    lock = SpecDecoder(look, wg, D, dw, mask_token_id=T.vocab - 1, budget=1)
+    out = [sd.prefill(prompt)]
+    assert lock.prefill(prompt) == out[0]
+    logits = torch.zeros(1, T.vocab, dtype=torch.bfloat16, device="cuda")
+    zero = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+    def one(tok):
+        am = look.verify(torch.tensor([tok], dtype=torch.int32), torch.tensor([-1], dtype=torch.int32), logits_out=logits)
+        look.commit(zero, torch.stack([torch.ones((), dtype=torch.int32, device="cuda"), am[0]]).to(torch.int32))
+        return int(am[0].item())
+
+    ahead = []
+    real_forward = sd.draft.forward
+
+    def knowing_forward(noise, window):
+        hidden, lg = real_forward(noise, window)              # the real kernels still run; only the proposal is replaced
+        lg = torch.full_like(lg, -4.0)
+        for j in range(1, D.q_len):
+            lg[j, ahead[j - 1]] = 8.0
+        return hidden, lg
+    sd.draft.forward = knowing_forward
+    near_ties = 0
+    while len(out) < n_gen:
+        root = sd.last_token
+        snap = (look.k_cache.clone(), look.v_cache.clone(), look.ssm_state.clone(), look.conv_state.clone(), look.past)
+        ahead.clear(); tok = root
+        for _ in range(D.q_len - 1):
+            tok = one(tok); ahead.append(tok)
+        look.k_cache.copy_(snap[0]); look.v_cache.copy_(snap[1]); look.ssm_state.copy_(snap[2]); look.conv_state.copy_(snap[3]); look.past = snap[4]
+        new = sd.step()
+        tok = root
+        for t_new in new:                                     # replay the round on the lockstep target, token by token
+            am = one(tok)
+            lg = logits[0].float()
+            if t_new != am:
+                near_ties += 1
+                assert float(lg.max() - lg[t_new]) <= 2 * LOGIT_NOISE, (len(out), t_new, am)
+            tok = t_new
+        assert look.past == sd.target.past
+        out.extend(new)
+    sd.target.check_status()
+    per_round = sd.stats["committed"] / sd.stats["steps"]
+    print(f"knowing draft: {sd.stats['steps']} rounds for {len(out)} tokens, {per_round:.1f} committed per round, {near_ties} near-tie choices")
+    assert per_round >= 2.0
 
 
 def test_spec_loop_argument_checks():

@@ -345,3 +345,76 @@ def test_feature_ring_capture_and_commit():
     for i in range(n):
         for k in range(len(layers)):
             assert torch.equal(win[i, k * D.hidden:(k + 1) * D.hidden], history[tt.past - n + i][k])
+
+
+@pytest.mark.parametrize("n_ctx,n_nodes,seed", [(70, 14, 21), (130, 33, 22), (0, 5, 23)])
+def test_tree_verify_with_q8_0_kv_cache(n_ctx, n_nodes, seed):
+    """The reference's default cache type: K / V rows are Q8_0 (quantised in the kernel from the f32 row, read back as
+    bf16(d * q)).  Same flow as the bf16 test against the oracle run with the same cache arithmetic; the committed cache
+    rows are compared after dequantisation (at most one quantisation step apart)."""
+    from oracle.tree_verify_oracle import TreeOracle, q8_0_dequant, q8_0_quant
+    from qwen35_b200.tree_verify import TreeTarget, make_random_tree_weights, random_tree
+    D = small_dims()
+    w = make_random_tree_weights(D, seed)
+    orc = TreeOracle(D, w, 256, kv_q8=True)
+    rng = np.random.default_rng(seed)
+    if n_ctx:
+        orc.feed(rng.integers(0, D.vocab, n_ctx))
+    wg = {"layers": [{k: v.cuda() for k, v in L.items()} for L in w["layers"]],
+          "token_embd": w["token_embd"].cuda(), "output_norm": w["output_norm"].cuda(), "output_w": w["output_w"].cuda()}
+    tt = TreeTarget(D, wg, max_ctx=256, kv_type="q8_0")
+    assert tt.k_cache.dtype == torch.uint8 and tt.k_cache.shape[-1] == 272
+    for i in range(D.n_fa):
+        if n_ctx:
+            tt.k_cache[i, :, :n_ctx] = torch.from_numpy(q8_0_quant(orc.k[i].numpy())).cuda()
+            tt.v_cache[i, :, :n_ctx] = torch.from_numpy(q8_0_quant(orc.v[i].numpy())).cuda()
+    for i in range(D.n_dn):
+        tt.ssm_state[i] = orc.ssm[i].cuda(); tt.conv_state[i] = orc.conv[i].cuda()
+    tt.past = n_ctx
+    parents = random_tree(n_nodes, 6, seed)
+    tokens = rng.integers(0, D.vocab, n_nodes)
+    ref_logits, ctxs, hids = orc.verify(tokens, parents)
+    teacher = torch.zeros(D.n_layers, n_nodes, D.hidden, dtype=torch.bfloat16)
+    for t in range(n_nodes):
+        for il in range(1, D.n_layers):
+            teacher[il, t] = hids[t][il - 1].bfloat16()
+    dbg = torch.zeros(D.n_layers, n_nodes, D.hidden, dtype=torch.bfloat16, device="cuda")
+    tk, pr = torch.tensor(tokens, dtype=torch.int32), torch.tensor(parents, dtype=torch.int32)
+    tt.verify(tk, pr, dbg_hidden=dbg, dbg_teacher=teacher.cuda())
+    tt.check_status()
+    got_h = dbg.float().cpu()
+    ref_h = torch.stack([torch.stack(h) for h in hids]).transpose(0, 1)
+    assert float((got_h - ref_h).abs().max()) <= LAYER_ABS_TOL
+    print(f"q8_0 cache, teacher forced: {float((got_h == ref_h).float().mean()):.4%} of layer outputs bit-identical")
+    # the rows the verify wrote (teacher forced, so their inputs equal the oracle's): node t sits at slot past + t.  An
+    # f32 last-place difference in a row's values may move one element across a rounding boundary
+    flipped = total = 0
+    for i in range(D.n_fa):
+        for t in range(n_nodes):
+            for cache, key in ((tt.k_cache, "k"), (tt.v_cache, "v")):
+                ref = ctxs[t][key][i][:, -1]                                                         # [kv_heads, 256]
+                got = torch.from_numpy(q8_0_dequant(cache[i, :, n_ctx + t].cpu().numpy()))
+                step = ref.reshape(ref.shape[0], -1, 32).abs().amax(-1, keepdim=True) / 127
+                d = (got - ref).reshape(ref.shape[0], -1, 32).abs()
+                tol = 1e-6
+                assert bool((d <= step * 1.01 + tol).all()), (i, t, key)
+                flipped += int((d > tol).sum()); total += d.numel()
+    print(f"q8_0 cache rows: {flipped}/{total} elements one quantisation step from the oracle's")
+    assert flipped <= 0.02 * total
+    logits = torch.zeros(n_nodes, D.vocab, dtype=torch.bfloat16, device="cuda")
+    am = tt.verify(tk, pr, logits_out=logits).cpu().clone()
+    tt.check_status()
+    for t in range(n_nodes):
+        assert float((logits[t].float().cpu() - ref_logits[t]).abs().max()) <= LOGIT_TOL
+    # walk the root's first child if the arg-max allows, else just the root; commit; compare the dequantised cache rows
+    path, result = tt.accept()
+    ref_path, ref_next = TreeOracle.accept(tokens, parents, am.tolist())
+    n_acc = tt.commit()
+    orc.commit(ctxs, ref_path)
+    assert n_acc == len(ref_path) and tt.past == orc.past
+    for i in range(D.n_fa):
+        for cache, ref in ((tt.k_cache, orc.k[i]), (tt.v_cache, orc.v[i])):
+            got = torch.from_numpy(q8_0_dequant(cache[i, :, :tt.past].cpu().numpy()))
+            step = ref.reshape(ref.shape[0], ref.shape[1], -1, 32).abs().amax(-1, keepdim=True) / 127
+            d = (got - ref).reshape(ref.shape[0], ref.shape[1], -1, 32).abs()
+            assert bool((d <= step * 1.01 + 2.0 ** -5).all())          # the bf16 test's free-running bound plus one quantisation step
