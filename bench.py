@@ -376,6 +376,12 @@ def run_ours(args):
         raise SystemExit("bench.py needs a CUDA device (there is no CPU fallback)")
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
+    if args.only:
+        # one section alone (for profiling a path without the others' launches): prints that section's JSON, not the bench line
+        if rank == 0:
+            fn = {"draft_forward": draft_forward_bench, "tree_verify": tree_verify_bench}[args.only]
+            print(json.dumps({args.only: fn(dev, iters=max(1, args.steps))}))
+        return
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev)
@@ -554,6 +560,8 @@ def main():
     ap.add_argument("--batched-groups", type=int, default=1, help="concurrent sub-batches of the batched-decode step (1 = one batch)")
     ap.add_argument("--kernel-table", action="store_true", help="print the per-kernel device times of one batched step to stderr")
     ap.add_argument("--prefill-sweep", default="128,512,1024,4096", help="prompt lengths of the prefill sweep ('' = skip)")
+    ap.add_argument("--only", choices=["draft_forward", "tree_verify"], default=None,
+                    help="run just this section with --steps timed iterations and print its JSON (profiling aid; not the bench line)")
     ap.add_argument("--tree-verify", type=int, default=1, help="run the 27B-class tree-verify section (0 = skip)")
     ap.add_argument("--prompt", type=int, default=520, help="prompt tokens (smaller values are for profiler captures)")
     ap.add_argument("--gen", type=int, default=128, help="decode tokens per step")
