@@ -426,6 +426,7 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();      // barriers, TMEM and tensor maps are set up; from here on the kernel touches its predecessor's outputs
 
     if (warp == 0) {
         // activation tiles: k-step i may be issued as soon as the MMAs of k-step i - STAGES have read the stage
@@ -782,10 +783,12 @@ int gemm_q4k(const bf16* A, int lda, const uint8_t* W, int w_rows, bf16* C, int 
     cfg.blockDim = dim3(Q4K_THREADS);
     cfg.dynamicSmemBytes = Q4K_SMEM;
     cfg.stream = stream;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = 1; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = (unsigned)split;
-    cfg.attrs = at; cfg.numAttrs = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at; cfg.numAttrs = g_pdl_launch ? 2 : 1;
 #define Q35_GEMM_Q4K(E)                                                                                                            \
     case E: {                                                                                                                      \
         static bool attr = false;                                                                                                  \

@@ -14,6 +14,7 @@ static int g_sms[MAX_DEVICES] = {};
 static std::mutex g_mu;
 static thread_local char g_err[512] = "";
 std::atomic<long long> g_launches{0};
+bool g_pdl_launch = false;
 
 void set_error(const char* fmt, ...) {
     va_list ap;

@@ -20,6 +20,9 @@ void register_status_word(int* dev_ptr);
 int device_sm_count();
 void set_error(const char* fmt, ...);
 extern std::atomic<long long> g_launches;
+// set by a caller whose every kernel begins with pdl_wait(): the GEMM launchers then add the programmatic-stream-
+// serialization attribute to their launches (the GEMM kernels call pdl_wait() after their prologue)
+extern bool g_pdl_launch;
 
 #define Q35_CUDA_OK(expr)                                                         \
     do {                                                                          \

@@ -95,6 +95,7 @@ __global__ void __launch_bounds__(256) tv_dequant_q4k_kernel(const uint8_t* __re
 // embedding rows of the node tokens, bf16
 __global__ void __launch_bounds__(32) tv_embed_q4k_kernel(const uint8_t* __restrict__ embd, const int* __restrict__ tokens, int hidden,
                                                           bf16* __restrict__ out) {
+    pdl_wait();
     const int t = blockIdx.x, blk = blockIdx.y, lane = threadIdx.x;
     const size_t b = (size_t)tokens[t] * (hidden / 256) + blk;
     float lo[4], hi[4];
@@ -116,6 +117,7 @@ __global__ void __launch_bounds__(32) tv_embed_q4k_kernel(const uint8_t* __restr
 constexpr int TV_DN_SLOTS = 8;
 __global__ void tv_tree_prep_kernel(const int* __restrict__ parents, int n, int* __restrict__ depth, unsigned long long* __restrict__ anc,
                                     int* __restrict__ src, int* __restrict__ save) {
+    pdl_wait();
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
     int last[TV_MAX_NODES], owner[TV_DN_SLOTS];
     for (int t = 0; t < n; ++t) {
@@ -211,6 +213,7 @@ __device__ __forceinline__ void tv_finish_rows(bf16* tile, const unsigned char* 
 __global__ void __launch_bounds__(128) tv_fa_prep_kernel(const bf16* __restrict__ proj, int ldp, const float* __restrict__ qn, const float* __restrict__ kn,
                                                          const int* __restrict__ depth, TvDims D, int past, int max_ctx,
                                                          bf16* __restrict__ qbuf, unsigned char* __restrict__ k_cache, unsigned char* __restrict__ v_cache, int kv_type) {
+    pdl_wait();
     __shared__ float red[4];
     __shared__ float xs[TV_HD];
     const int t = blockIdx.x, slot = blockIdx.y, tid = threadIdx.x;
@@ -270,6 +273,7 @@ template <bool Q8>
 __global__ void __launch_bounds__(256, 1) tv_att_scores_kernel(const bf16* __restrict__ qbuf, const unsigned char* __restrict__ k_cache,
                                                                const unsigned long long* __restrict__ anc, TvDims D, int n_nodes, int past,
                                                                int max_ctx, int lpad, float* __restrict__ scores) {
+    pdl_wait();
     extern __shared__ __align__(16) unsigned char tv_smem[];
     bf16* Qs = reinterpret_cast<bf16*>(tv_smem);
     const int gqa = D.q_heads / D.kv_heads, R = n_nodes * gqa, mt_n = (R + 15) / 16;
@@ -331,6 +335,7 @@ __global__ void __launch_bounds__(256, 1) tv_att_scores_kernel(const bf16* __res
 
 // softmax statistics of every query row over the whole (masked) key range: one warp per row
 __global__ void __launch_bounds__(256) tv_att_stats_kernel(const float* __restrict__ scores, int rows, int lpad, int len, float* __restrict__ stats) {
+    pdl_wait();
     const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (r >= rows) return;
     const float* s = scores + (size_t)r * lpad;
@@ -358,6 +363,7 @@ __global__ void __launch_bounds__(256) tv_att_stats_kernel(const float* __restri
 template <bool Q8>
 __global__ void __launch_bounds__(256, 1) tv_att_pv_kernel(const unsigned char* __restrict__ v_cache, const float* __restrict__ scores, const float* __restrict__ stats,
                                                            TvDims D, int n_nodes, int past, int max_ctx, int lpad, float* __restrict__ partial) {
+    pdl_wait();
     extern __shared__ __align__(16) unsigned char tv_smem[];
     bf16* Vs = reinterpret_cast<bf16*>(tv_smem);                     // [TV_CHUNK keys][TV_QSTRIDE]
     bf16* Ps = Vs + (size_t)TV_CHUNK * TV_QSTRIDE;                   // [rows][TV_PSTRIDE keys]
@@ -418,6 +424,7 @@ __global__ void __launch_bounds__(256, 1) tv_att_pv_kernel(const unsigned char* 
 // sum of the chunk partials in chunk order, times sigmoid(gate), one rounding to bf16.  grid (nodes, q_heads), 128 threads
 __global__ void __launch_bounds__(128) tv_att_merge_kernel(const float* __restrict__ partial, const bf16* __restrict__ proj, int ldp, TvDims D,
                                                            int n_nodes, int n_chunks, bf16* __restrict__ out) {
+    pdl_wait();
     const int t = blockIdx.x, hq = blockIdx.y, tid = threadIdx.x;
     const int gqa = D.q_heads / D.kv_heads, R = n_nodes * gqa, kvh = hq / gqa, r = t * gqa + hq % gqa;
     const float* pb = partial + ((size_t)kvh * R + r) * n_chunks * TV_HD;
@@ -445,6 +452,7 @@ __global__ void __launch_bounds__(128) tv_dn_conv_norm_kernel(const bf16* __rest
                                                               const bf16* __restrict__ ba, int ldba, const float* __restrict__ ssm_a,
                                                               const float* __restrict__ dt_bias, TvDims D, float* __restrict__ qkv,
                                                               float* __restrict__ node_conv, float* __restrict__ gate /* [nodes][v_heads][2] */) {
+    pdl_wait();
     __shared__ float red[4];
     const int t = blockIdx.x, hb = blockIdx.y, tid = threadIdx.x, ch = hb * TV_DN + tid;
     float x[4];
@@ -492,6 +500,7 @@ __global__ void __launch_bounds__(128) tv_dn_tree_kernel(const float* __restrict
                                                          const int* __restrict__ parents, const int* __restrict__ src, const int* __restrict__ save,
                                                          int n_nodes, TvDims D, const float* __restrict__ ssm_state, __half* __restrict__ node_states,
                                                          float* __restrict__ core) {
+    pdl_wait();
     extern __shared__ __align__(16) unsigned char tv_smem[];
     float* sq = reinterpret_cast<float*>(tv_smem);                       // [n][128]
     float* sk = sq + (size_t)n_nodes * TV_DN;                             // [n][128]
@@ -581,6 +590,7 @@ __global__ void __launch_bounds__(128) tv_dn_tree_kernel(const float* __restrict
 // gated norm: y = bf16(o * rsqrt(mean o^2 + eps) * w * silu(z)).  grid (nodes, v_heads), 128 threads
 __global__ void __launch_bounds__(128) tv_dn_gated_norm_kernel(const float* __restrict__ core, const bf16* __restrict__ proj, int ldp, int z_off,
                                                                const float* __restrict__ w, TvDims D, bf16* __restrict__ out) {
+    pdl_wait();
     __shared__ float red[4];
     const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
     const float o = core[((size_t)t * D.dn_v_heads + h) * TV_DN + tid];
@@ -592,6 +602,7 @@ __global__ void __launch_bounds__(128) tv_dn_gated_norm_kernel(const float* __re
 // ------------------------------------------- head and walk -------------------------------------------
 // arg-max of every node's bf16 logits, lowest index among equal maxima.  grid nodes, 1024 threads
 __global__ void __launch_bounds__(1024) tv_argmax_kernel(const bf16* __restrict__ logits, int vocab, int* __restrict__ out) {
+    pdl_wait();
     __shared__ float sv[32];
     __shared__ int si[32];
     const bf16* row = logits + (size_t)blockIdx.x * vocab;
@@ -688,6 +699,7 @@ __global__ void tv_commit_kv_kernel(unsigned char* __restrict__ k_cache, unsigne
 // feature capture: rows of `hidden` (node t) -> ring row (past + t) % cap, column block k.  grid nodes, 256 threads
 __global__ void __launch_bounds__(256) tv_capture_kernel(const bf16* __restrict__ hidden, int H, int past, int cap, int row_elems, int col0,
                                                          bf16* __restrict__ ring) {
+    pdl_wait();
     const int t = blockIdx.x;
     const uint4* src = reinterpret_cast<const uint4*>(hidden + (size_t)t * H);
     uint4* dst = reinterpret_cast<uint4*>(ring + (size_t)((past + t) % cap) * row_elems + col0);
@@ -715,6 +727,20 @@ struct TvScratch {
 };
 
 static size_t align_up(size_t v) { return (v + 255) & ~(size_t)255; }
+
+// launch with the programmatic-stream-serialization attribute: the kernel may be scheduled while its predecessor in the
+// stream drains (every kernel launched this way starts with pdl_wait()).  Hides most of the 2-3 us between the ~660
+// dependent launches of a pass.
+template <typename... KArgs, typename... Args>
+static cudaError_t tv_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid; cfg.blockDim = block; cfg.dynamicSmemBytes = smem; cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at; cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 
 static TvScratch tv_layout(const TvDims& D, int n, int max_ctx, char* base) {
     TvScratch s;
@@ -755,6 +781,7 @@ static int q4k_linear(const bf16* X, int lda, const void* W, bool dense, int out
 
 // embedding rows from a dense bf16 table
 __global__ void __launch_bounds__(256) tv_embed_dense_kernel(const bf16* __restrict__ embd, const int* __restrict__ tokens, int hidden, bf16* __restrict__ out) {
+    pdl_wait();
     const bf16* src = embd + (size_t)tokens[blockIdx.x] * hidden;
     for (int i = threadIdx.x; i < hidden; i += 256) out[(size_t)blockIdx.x * hidden + i] = src[i];
 }
@@ -846,9 +873,10 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
         return QWEN35_ERR_BAD_ARG;
     }
 
-    tv_tree_prep_kernel<<<1, 32, 0, stream>>>(in->parents, n, s.depth, s.anc, s.dn_src, s.dn_save);
-    if (in->dense_mask & 1u) tv_embed_dense_kernel<<<n, 256, 0, stream>>>((const bf16*)in->token_embd, in->node_tokens, D.hidden, s.hidden);
-    else tv_embed_q4k_kernel<<<dim3(n, D.hidden / 256), 32, 0, stream>>>((const uint8_t*)in->token_embd, in->node_tokens, D.hidden, s.hidden);
+    struct PdlGuard { PdlGuard() { g_pdl_launch = true; } ~PdlGuard() { g_pdl_launch = false; } } pdl_guard;      // the Q4_K GEMM launches join in
+    Q35_CUDA_OK(tv_launch(tv_tree_prep_kernel, 1, 32, 0, stream, in->parents, n, s.depth, s.anc, s.dn_src, s.dn_save));
+    if (in->dense_mask & 1u) Q35_CUDA_OK(tv_launch(tv_embed_dense_kernel, n, 256, 0, stream, (const bf16*)in->token_embd, in->node_tokens, D.hidden, s.hidden));
+    else Q35_CUDA_OK(tv_launch(tv_embed_q4k_kernel, dim3(n, D.hidden / 256), 32, 0, stream, (const uint8_t*)in->token_embd, in->node_tokens, D.hidden, s.hidden));
     g_launches.fetch_add(2);
     const int n_layers = in->dbg_num_layers > 0 && in->dbg_num_layers < D.n_layers ? in->dbg_num_layers : D.n_layers;
     int i_fa = 0, i_dn = 0;
@@ -857,21 +885,21 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
         const bool is_fa = (il % D.fa_period) == D.fa_period - 1;
         if (il > 0 && in->dbg_teacher)
             Q35_CUDA_OK(cudaMemcpyAsync(s.hidden, (const bf16*)in->dbg_teacher + (size_t)il * n * D.hidden, (size_t)n * D.hidden * 2, cudaMemcpyDeviceToDevice, stream));
-        tv_rmsnorm_kernel<<<n, 256, 0, stream>>>(s.hidden, (const float*)W.attn_norm, s.normed, D.hidden, D.eps);
+        Q35_CUDA_OK(tv_launch(tv_rmsnorm_kernel, n, 256, 0, stream, s.hidden, (const float*)W.attn_norm, s.normed, D.hidden, D.eps));
         g_launches.fetch_add(1);
         int att_w;
         if (is_fa) {
             Q35_TRYT(q4k_linear(s.normed, D.hidden, W.w_in, (W.dense_mask & 1u) != 0, fa_in, D.hidden, s.proj, fa_in, nullptr, 0, n, 0, stream));
             unsigned char* kc = (unsigned char*)in->k_cache + (size_t)i_fa * kv_layer;
             unsigned char* vc = (unsigned char*)in->v_cache + (size_t)i_fa * kv_layer;
-            tv_fa_prep_kernel<<<dim3(n, D.q_heads + 2 * D.kv_heads), 128, 0, stream>>>(s.proj, fa_in, (const float*)W.q_norm, (const float*)W.k_norm, s.depth, D,
-                                                                                       in->past, in->max_ctx, s.qbuf, kc, vc, in->kv_type);
-            if (q8) tv_att_scores_kernel<true><<<dim3(chunks, D.kv_heads), 256, sc_smem + q8_raw, stream>>>(s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores);
-            else tv_att_scores_kernel<false><<<dim3(chunks, D.kv_heads), 256, sc_smem, stream>>>(s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores);
-            tv_att_stats_kernel<<<(D.kv_heads * R + 7) / 8, 256, 0, stream>>>(s.scores, D.kv_heads * R, lpad, chunks * TV_CHUNK, s.stats);
-            if (q8) tv_att_pv_kernel<true><<<dim3(chunks, D.kv_heads), 256, pv_smem + q8_raw, stream>>>(vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial);
-            else tv_att_pv_kernel<false><<<dim3(chunks, D.kv_heads), 256, pv_smem, stream>>>(vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial);
-            tv_att_merge_kernel<<<dim3(n, D.q_heads), 128, 0, stream>>>(s.partial, s.proj, fa_in, D, n, chunks, s.attn);
+            Q35_CUDA_OK(tv_launch(tv_fa_prep_kernel, dim3(n, D.q_heads + 2 * D.kv_heads), 128, 0, stream, s.proj, fa_in, (const float*)W.q_norm, (const float*)W.k_norm, s.depth, D,
+                                                                                       in->past, in->max_ctx, s.qbuf, kc, vc, in->kv_type));
+            if (q8) Q35_CUDA_OK(tv_launch(tv_att_scores_kernel<true>, dim3(chunks, D.kv_heads), 256, sc_smem + q8_raw, stream, s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores));
+            else Q35_CUDA_OK(tv_launch(tv_att_scores_kernel<false>, dim3(chunks, D.kv_heads), 256, sc_smem, stream, s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores));
+            Q35_CUDA_OK(tv_launch(tv_att_stats_kernel, (D.kv_heads * R + 7) / 8, 256, 0, stream, s.scores, D.kv_heads * R, lpad, chunks * TV_CHUNK, s.stats));
+            if (q8) Q35_CUDA_OK(tv_launch(tv_att_pv_kernel<true>, dim3(chunks, D.kv_heads), 256, pv_smem + q8_raw, stream, vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial));
+            else Q35_CUDA_OK(tv_launch(tv_att_pv_kernel<false>, dim3(chunks, D.kv_heads), 256, pv_smem, stream, vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial));
+            Q35_CUDA_OK(tv_launch(tv_att_merge_kernel, dim3(n, D.q_heads), 128, 0, stream, s.partial, s.proj, fa_in, D, n, chunks, s.attn));
             g_launches.fetch_add(5);
             att_w = D.q_heads * TV_HD;
             ++i_fa;
@@ -886,17 +914,17 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
             float* nconv = (float*)in->node_conv + (size_t)i_dn * nconv_layer;
             __half* nstates = (__half*)in->node_states + (size_t)i_dn * nstate_layer;
             Q35_CUDA_OK(cudaStreamWaitEvent(stream, side.join, 0));
-            tv_dn_conv_norm_kernel<<<dim3(n, conv_ch / TV_DN), 128, 0, stream>>>(s.proj, dn_in, in->parents, cstate, (const float*)W.conv_w, conv_ch, s.ba, 2 * D.dn_v_heads,
-                                                                              (const float*)W.ssm_a, (const float*)W.dt_bias, D, s.dn_qkv, nconv, s.dn_gate);
-            tv_dn_tree_kernel<<<dim3(D.dn_v_heads, TV_DN / 16), 128, tv_dn_tree_smem(n), stream>>>(s.dn_qkv, conv_ch, s.dn_gate, in->parents, s.dn_src, s.dn_save, n, D,
-                                                                                 (const float*)in->ssm_state + (size_t)i_dn * state_layer, nstates, s.core);
-            tv_dn_gated_norm_kernel<<<dim3(n, D.dn_v_heads), 128, 0, stream>>>(s.core, s.proj, dn_in, z_off, (const float*)W.ssm_norm, D, s.attn);
+            Q35_CUDA_OK(tv_launch(tv_dn_conv_norm_kernel, dim3(n, conv_ch / TV_DN), 128, 0, stream, s.proj, dn_in, in->parents, cstate, (const float*)W.conv_w, conv_ch, s.ba, 2 * D.dn_v_heads,
+                                                                              (const float*)W.ssm_a, (const float*)W.dt_bias, D, s.dn_qkv, nconv, s.dn_gate));
+            Q35_CUDA_OK(tv_launch(tv_dn_tree_kernel, dim3(D.dn_v_heads, TV_DN / 16), 128, tv_dn_tree_smem(n), stream, s.dn_qkv, conv_ch, s.dn_gate, in->parents, s.dn_src, s.dn_save, n, D,
+                                                                                 (const float*)in->ssm_state + (size_t)i_dn * state_layer, nstates, s.core));
+            Q35_CUDA_OK(tv_launch(tv_dn_gated_norm_kernel, dim3(n, D.dn_v_heads), 128, 0, stream, s.core, s.proj, dn_in, z_off, (const float*)W.ssm_norm, D, s.attn));
             g_launches.fetch_add(3);
             att_w = D.dn_v_heads * TV_DN;
             ++i_dn;
         }
         Q35_TRYT(q4k_linear(s.attn, att_w, W.w_out, (W.dense_mask & 2u) != 0, D.hidden, att_w, s.resid, D.hidden, s.hidden, D.hidden, n, 1, stream));
-        tv_rmsnorm_kernel<<<n, 256, 0, stream>>>(s.resid, (const float*)W.post_norm, s.normed, D.hidden, D.eps);
+        Q35_CUDA_OK(tv_launch(tv_rmsnorm_kernel, n, 256, 0, stream, s.resid, (const float*)W.post_norm, s.normed, D.hidden, D.eps));
         g_launches.fetch_add(1);
         Q35_TRYT(q4k_linear(s.normed, D.hidden, W.w_gate_up, (W.dense_mask & 4u) != 0, D.ffn, D.hidden, s.mlp, D.ffn, nullptr, 0, n, 2, stream));
         Q35_TRYT(q4k_linear(s.mlp, D.ffn, W.w_down, (W.dense_mask & 8u) != 0, D.hidden, D.ffn, s.hidden, D.hidden, s.resid, D.hidden, n, 1, stream));
@@ -905,13 +933,13 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
         if (in->target_feat)
             for (int k = 0; k < in->n_capture; ++k)
                 if (in->capture_layers[k] == il) {
-                    tv_capture_kernel<<<n, 256, 0, stream>>>(s.hidden, D.hidden, in->past, in->feat_cap, in->n_capture * D.hidden, k * D.hidden, (bf16*)in->target_feat);
+                    Q35_CUDA_OK(tv_launch(tv_capture_kernel, n, 256, 0, stream, s.hidden, D.hidden, in->past, in->feat_cap, in->n_capture * D.hidden, k * D.hidden, (bf16*)in->target_feat));
                     g_launches.fetch_add(1);
                 }
     }
-    tv_rmsnorm_kernel<<<n, 256, 0, stream>>>(s.hidden, (const float*)in->output_norm, s.normed, D.hidden, D.eps);
+    Q35_CUDA_OK(tv_launch(tv_rmsnorm_kernel, n, 256, 0, stream, s.hidden, (const float*)in->output_norm, s.normed, D.hidden, D.eps));
     Q35_TRYT(q4k_linear(s.normed, D.hidden, in->output_w, (in->dense_mask & 2u) != 0, D.vocab, D.hidden, s.logits, D.vocab, nullptr, 0, n, 0, stream));
-    tv_argmax_kernel<<<n, 1024, 0, stream>>>(s.logits, D.vocab, in->node_argmax);
+    Q35_CUDA_OK(tv_launch(tv_argmax_kernel, n, 1024, 0, stream, s.logits, D.vocab, in->node_argmax));
     g_launches.fetch_add(2);
     if (in->logits_out) Q35_CUDA_OK(cudaMemcpyAsync(in->logits_out, s.logits, (size_t)n * D.vocab * 2, cudaMemcpyDeviceToDevice, stream));
     Q35_CUDA_OK(cudaGetLastError());
