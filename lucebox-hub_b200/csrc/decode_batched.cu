@@ -40,6 +40,7 @@ __global__ void __launch_bounds__(256) bd_dn_step_kernel(const bf16* __restrict_
                                                          const bf16* __restrict__ a_log, const bf16* __restrict__ dt_bias,
                                                          const float* __restrict__ conv, size_t conv_seq_stride,
                                                          float* __restrict__ state, size_t state_seq_stride, bf16* __restrict__ core_out) {
+    pdl_wait();
     __shared__ __align__(16) float sqk[2][DN_K];
     __shared__ float red[2][4];
     __shared__ float shd[2];
@@ -101,6 +102,7 @@ __global__ void __launch_bounds__(256) bd_dn_step_kernel(const bf16* __restrict_
 
 // conv window shift for every (sequence, channel), after all readers of the old window have finished
 __global__ void bd_conv_shift_kernel(const bf16* __restrict__ proj, int ldp, float* __restrict__ conv, size_t conv_seq_stride, int B) {
+    pdl_wait();
     const int idx = blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= B * DN_CONV_CH) return;
     const int b = idx / DN_CONV_CH, ch = idx % DN_CONV_CH;
@@ -119,6 +121,7 @@ __global__ void __launch_bounds__(256) bd_qk_norm_rope_kernel(const bf16* __rest
                                                               const bf16* __restrict__ kn_w, const RopeTable inv_freq,
                                                               const int* __restrict__ positions, const int* __restrict__ table, int max_pages,
                                                               bf16* __restrict__ q_out, bf16* __restrict__ k_pages, bf16* __restrict__ v_pages, int B) {
+    pdl_wait();
     const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (gw >= B * 12) return;
     const int b = gw / 12, slot = gw % 12, pos = positions[b];
@@ -194,6 +197,7 @@ __device__ __forceinline__ void bd_stage_rows(const bf16* __restrict__ pages, co
 __global__ void __launch_bounds__(128) bd_att_scores_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k_pages,
                                                             const int* __restrict__ positions, const int* __restrict__ table, int max_pages,
                                                             float* __restrict__ scores, float* __restrict__ stats, int max_ctx, int max_chunks) {
+    pdl_wait();
     extern __shared__ __align__(16) unsigned char bd_sm[];
     __shared__ float ssc[FA_GQA][BD_CHUNK];
     bf16* Qs = reinterpret_cast<bf16*>(bd_sm);           // [16][BD_LD], rows 0-3 = the q heads of this kv head
@@ -259,6 +263,7 @@ __global__ void __launch_bounds__(128) bd_att_scores_kernel(const bf16* __restri
 __global__ void __launch_bounds__(128) bd_att_pv_kernel(const bf16* __restrict__ v_pages, const int* __restrict__ positions,
                                                         const int* __restrict__ table, int max_pages, const float* __restrict__ scores,
                                                         const float* __restrict__ stats, float* __restrict__ partial, int max_ctx, int max_chunks) {
+    pdl_wait();
     extern __shared__ __align__(16) unsigned char bd_sm[];
     __shared__ float sml[FA_GQA][2];
     bf16* Vs = reinterpret_cast<bf16*>(bd_sm);           // [BD_CHUNK][BD_LD]
@@ -315,6 +320,7 @@ __global__ void __launch_bounds__(128) bd_att_pv_kernel(const bf16* __restrict__
 
 __global__ void __launch_bounds__(256) bd_att_merge_kernel(const float* __restrict__ partial, const int* __restrict__ positions,
                                                            const bf16* __restrict__ proj, int ldp, bf16* __restrict__ out, int B, int max_chunks) {
+    pdl_wait();
     const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (gw >= B * FA_Q_HEADS) return;
     const int b = gw / FA_Q_HEADS, head = gw % FA_Q_HEADS;
@@ -339,6 +345,7 @@ __global__ void __launch_bounds__(256) bd_att_merge_kernel(const float* __restri
 
 // ---- per-row arg-max over bf16 logits [B, VOCAB]: one CTA per row ---------------------------------------
 __global__ void __launch_bounds__(1024) bd_argmax_kernel(const bf16* __restrict__ logits, int* __restrict__ out_tokens, int* __restrict__ positions) {
+    pdl_wait();
     __shared__ float sv[32];
     __shared__ int si[32];
     const int b = blockIdx.x, tid = threadIdx.x;
@@ -371,6 +378,7 @@ __global__ void __launch_bounds__(1024) bd_argmax_kernel(const bf16* __restrict_
 
 // debug / teacher forcing helpers
 __global__ void bd_copy_rows_kernel(const bf16* __restrict__ src, bf16* __restrict__ dst, int n_u4) {
+    pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n_u4) reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
 }
@@ -483,24 +491,27 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
     const int n_layers = in->dbg_num_layers > 0 ? in->dbg_num_layers : NUM_LAYERS;
     const size_t page_layer_stride = (size_t)in->num_pages * FA_KV_HEADS * KV_PAGE * FA_HEAD_DIM;
 
+    // a step is ~300 dependent launches (replayed as a CUDA graph): programmatic dependent launch lets each kernel be
+    // scheduled while its predecessor drains; every kernel of the step starts with pdl_wait()
+    PdlGuard pdl_guard;
     int i_dn = 0, i_fa = 0;
     for (int layer = 0; layer < n_layers; ++layer) {
         const LayerRec& L = layers_h[layer];
         const PrefillFusedB& F = fused_h[layer];
         if (layer > 0 && in->dbg_teacher)
-            bd_copy_rows_kernel<<<(int)((n_hidden / 8 + 255) / 256), 256, 0, stream>>>((const bf16*)in->dbg_teacher + (size_t)layer * n_hidden, hidden, (int)(n_hidden / 8));
-        pf_rmsnorm_kernel<<<B, 128, 0, stream>>>(layer == 0 ? in->tokens_in : nullptr, (const bf16*)in->embed_weight, hidden, (const bf16*)L.p[0],
-                                                 layer == 0 ? hidden : nullptr, normed, B);
+            Q35_CUDA_OK(pdl_launch(bd_copy_rows_kernel, (int)((n_hidden / 8 + 255) / 256), 256, 0, stream, (const bf16*)in->dbg_teacher + (size_t)layer * n_hidden, hidden, (int)(n_hidden / 8)));
+        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, B, 128, 0, stream, layer == 0 ? in->tokens_in : nullptr, (const bf16*)in->embed_weight, hidden, (const bf16*)L.p[0],
+                                                 layer == 0 ? hidden : nullptr, normed, B));
         const bf16 *w_out, *w_post, *w_down;
         if (L.type == 0) {
             const int ldp = DN_PROJ_ROWS;
             Q35_TRYB(gemm_bf16(normed, HIDDEN, (const bf16*)F.proj_weight, DN_PROJ_ROWS, proj, ldp, nullptr, 0, B, DN_PROJ_ROWS, HIDDEN, 0, 0, stream));
             float* conv = (float*)in->conv_bufs + (size_t)i_dn * DN_CONV_CH * 4;
             float* state = (float*)in->dn_states + (size_t)i_dn * DN_HEADS * DN_V * DN_K;
-            bd_dn_step_kernel<<<dim3(B, DN_HEADS, DN_V / BD_DN_ROWS), 256, 0, stream>>>(proj, ldp, (const bf16*)L.p[DN_CONV], (const bf16*)L.p[DN_ALOG],
-                                                                                  (const bf16*)L.p[DN_DTBIAS], conv, conv_stride, state, state_stride, core);
-            bd_conv_shift_kernel<<<(B * DN_CONV_CH + 255) / 256, 256, 0, stream>>>(proj, ldp, conv, conv_stride, B);
-            pf_gated_norm_kernel<<<(B * DN_HEADS + 7) / 8, 256, 0, stream>>>(core, proj, ldp, (const bf16*)L.p[DN_NORM], attn, B);
+            Q35_CUDA_OK(pdl_launch(bd_dn_step_kernel, dim3(B, DN_HEADS, DN_V / BD_DN_ROWS), 256, 0, stream, proj, ldp, (const bf16*)L.p[DN_CONV], (const bf16*)L.p[DN_ALOG],
+                                                                                  (const bf16*)L.p[DN_DTBIAS], conv, conv_stride, state, state_stride, core));
+            Q35_CUDA_OK(pdl_launch(bd_conv_shift_kernel, (B * DN_CONV_CH + 255) / 256, 256, 0, stream, proj, ldp, conv, conv_stride, B));
+            Q35_CUDA_OK(pdl_launch(pf_gated_norm_kernel, (B * DN_HEADS + 7) / 8, 256, 0, stream, core, proj, ldp, (const bf16*)L.p[DN_NORM], attn, B));
             g_launches.fetch_add(3);
             w_out = (const bf16*)L.p[DN_OUT]; w_post = (const bf16*)L.p[DN_POST_NORM]; w_down = (const bf16*)L.p[DN_DOWN];
             ++i_dn;
@@ -509,27 +520,27 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
             Q35_TRYB(gemm_bf16(normed, HIDDEN, (const bf16*)F.proj_weight, FA_PROJ_ROWS, proj, ldp, nullptr, 0, B, FA_PROJ_ROWS, HIDDEN, 0, 0, stream));
             bf16* kp = (bf16*)in->k_pages + (size_t)i_fa * page_layer_stride;
             bf16* vp = (bf16*)in->v_pages + (size_t)i_fa * page_layer_stride;
-            bd_qk_norm_rope_kernel<<<(B * 12 + 7) / 8, 256, 0, stream>>>(proj, ldp, (const bf16*)L.p[FA_QNORM], (const bf16*)L.p[FA_KNORM], rt,
-                                                                         in->positions, in->block_table, in->max_pages, qbuf, kp, vp, B);
+            Q35_CUDA_OK(pdl_launch(bd_qk_norm_rope_kernel, (B * 12 + 7) / 8, 256, 0, stream, proj, ldp, (const bf16*)L.p[FA_QNORM], (const bf16*)L.p[FA_KNORM], rt,
+                                                                         in->positions, in->block_table, in->max_pages, qbuf, kp, vp, B));
             const dim3 agrid(B, FA_KV_HEADS, max_chunks);
-            bd_att_scores_kernel<<<agrid, 128, BD_SC_SMEM, stream>>>(qbuf, kp, in->positions, in->block_table, in->max_pages, att_scores, att_stats, in->max_ctx, max_chunks);
-            bd_att_pv_kernel<<<agrid, 128, BD_PV_SMEM, stream>>>(vp, in->positions, in->block_table, in->max_pages, att_scores, att_stats, att_part, in->max_ctx, max_chunks);
-            bd_att_merge_kernel<<<(B * FA_Q_HEADS + 7) / 8, 256, 0, stream>>>(att_part, in->positions, proj, ldp, attn, B, max_chunks);
+            Q35_CUDA_OK(pdl_launch(bd_att_scores_kernel, agrid, 128, BD_SC_SMEM, stream, qbuf, kp, in->positions, in->block_table, in->max_pages, att_scores, att_stats, in->max_ctx, max_chunks));
+            Q35_CUDA_OK(pdl_launch(bd_att_pv_kernel, agrid, 128, BD_PV_SMEM, stream, vp, in->positions, in->block_table, in->max_pages, att_scores, att_stats, att_part, in->max_ctx, max_chunks));
+            Q35_CUDA_OK(pdl_launch(bd_att_merge_kernel, (B * FA_Q_HEADS + 7) / 8, 256, 0, stream, att_part, in->positions, proj, ldp, attn, B, max_chunks));
             g_launches.fetch_add(4);
             w_out = (const bf16*)L.p[FA_O]; w_post = (const bf16*)L.p[FA_POST_NORM]; w_down = (const bf16*)L.p[FA_DOWN];
             ++i_fa;
         }
         Q35_TRYB(gemm_bf16(attn, 2048, w_out, HIDDEN, resid, HIDDEN, hidden, HIDDEN, B, HIDDEN, 2048, 1, 0, stream));
-        pf_rmsnorm_kernel<<<B, 128, 0, stream>>>(nullptr, nullptr, resid, w_post, nullptr, normed, B);
+        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, B, 128, 0, stream, nullptr, nullptr, resid, w_post, nullptr, normed, B));
         Q35_TRYB(gemm_bf16(normed, HIDDEN, (const bf16*)F.gate_up_weight, 2 * INTER, mlp, INTER, nullptr, 0, B, INTER, HIDDEN, 2, INTER, stream));
         Q35_TRYB(gemm_bf16(mlp, INTER, w_down, HIDDEN, hidden, HIDDEN, resid, HIDDEN, B, HIDDEN, INTER, 1, 0, stream));
         g_launches.fetch_add(2);
         if (in->dbg_hidden)
-            bd_copy_rows_kernel<<<(int)((n_hidden / 8 + 255) / 256), 256, 0, stream>>>(hidden, (bf16*)in->dbg_hidden + (size_t)layer * n_hidden, (int)(n_hidden / 8));
+            Q35_CUDA_OK(pdl_launch(bd_copy_rows_kernel, (int)((n_hidden / 8 + 255) / 256), 256, 0, stream, hidden, (bf16*)in->dbg_hidden + (size_t)layer * n_hidden, (int)(n_hidden / 8)));
     }
-    pf_rmsnorm_kernel<<<B, 128, 0, stream>>>(nullptr, nullptr, hidden, (const bf16*)in->final_norm_weight, nullptr, normed, B);
+    Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, B, 128, 0, stream, nullptr, nullptr, hidden, (const bf16*)in->final_norm_weight, nullptr, normed, B));
     Q35_TRYB(gemm_bf16(normed, HIDDEN, (const bf16*)in->lm_head_weight, VOCAB, logits, VOCAB, nullptr, 0, B, VOCAB, HIDDEN, 0, 0, stream));
-    bd_argmax_kernel<<<B, 1024, 0, stream>>>(logits, in->tokens_out, in->advance_positions ? in->positions : nullptr);
+    Q35_CUDA_OK(pdl_launch(bd_argmax_kernel, B, 1024, 0, stream, logits, in->tokens_out, in->advance_positions ? in->positions : nullptr));
     if (in->logits_out) Q35_CUDA_OK(cudaMemcpyAsync(in->logits_out, logits, n_logits * sizeof(bf16), cudaMemcpyDeviceToDevice, stream));
     g_launches.fetch_add(2);
     Q35_CUDA_OK(cudaGetLastError());

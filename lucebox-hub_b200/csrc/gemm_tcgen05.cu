@@ -246,6 +246,7 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem_base = *tmem_slot;
+    pdl_wait();      // barriers, TMEM and tensor maps are set up; from here on the kernel touches its predecessor's outputs
 
     if (warp == 0) {
         if (lane == 0) {
@@ -639,6 +640,18 @@ static bool make_tmap_q4k(CUtensorMap* tm, const void* ptr, int rows, int K) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// plain (non-cluster) launch of a GEMM kernel; joins a programmatic-dependent-launch chain when the caller asked for it
+template <typename K>
+static cudaError_t gemm_launch(K kernel, dim3 grid, size_t smem, cudaStream_t stream, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid; cfg.blockDim = dim3(GEMM_THREADS); cfg.dynamicSmemBytes = smem; cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at; cfg.numAttrs = g_pdl_launch ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, p);
+}
+
 // C[M,N] (row stride ldc) = epi(A[M,K] (row stride lda) . B[*,K]^T).  epi: 0 bf16, 1 + R, 2 silu(gate)*up with
 // gate rows [0,N) and up rows [up_row_offset, up_row_offset+N) of B.  b_rows = number of rows of B.
 int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ldc, const bf16* R, int ldr,
@@ -674,7 +687,7 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
                                              (int)gemm_smem(GEMM_STAGES_SKINNY)));                                                              \
             attr = true;                                                                                                                        \
         }                                                                                                                                       \
-        gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, false><<<grid, GEMM_THREADS, gemm_smem(GEMM_STAGES_SKINNY), stream>>>(tmA, tmB, p);      \
+        Q35_CUDA_OK(gemm_launch(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, false>, grid, gemm_smem(GEMM_STAGES_SKINNY), stream, tmA, tmB, p));      \
         break;                                                                                                                                  \
     }
         switch (epi) { Q35_GEMM_ROW2(EPI_BF16) Q35_GEMM_ROW2(EPI_RESIDUAL) Q35_GEMM_ROW2(EPI_SILU_MUL) }
@@ -689,7 +702,7 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
                                              (int)gemm_smem(GEMM_STAGES_WIDE)));                                                              \
             attr = true;                                                                                                                      \
         }                                                                                                                                     \
-        gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_WIDE, false><<<grid, GEMM_THREADS, gemm_smem(GEMM_STAGES_WIDE), stream>>>(tmA, tmB, p);        \
+        Q35_CUDA_OK(gemm_launch(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_WIDE, false>, grid, gemm_smem(GEMM_STAGES_WIDE), stream, tmA, tmB, p));        \
         break;                                                                                                                                \
     }
         switch (epi) { Q35_GEMM_WIDE(EPI_BF16) Q35_GEMM_WIDE(EPI_RESIDUAL) Q35_GEMM_WIDE(EPI_SILU_MUL) }
@@ -708,7 +721,7 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
                                              (int)gemm_smem(GEMM_STAGES_SKINNY)));                                                              \
             attr = true;                                                                                                                        \
         }                                                                                                                                       \
-        gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, false><<<grid, GEMM_THREADS, gemm_smem(GEMM_STAGES_SKINNY), stream>>>(tmA, tmB, p);      \
+        Q35_CUDA_OK(gemm_launch(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, false>, grid, gemm_smem(GEMM_STAGES_SKINNY), stream, tmA, tmB, p));      \
         break;                                                                                                                                  \
     }
             switch (epi) { Q35_GEMM_ROW(EPI_BF16) Q35_GEMM_ROW(EPI_RESIDUAL) Q35_GEMM_ROW(EPI_SILU_MUL) }
@@ -722,10 +735,12 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
         cfg.blockDim = dim3(GEMM_THREADS);
         cfg.dynamicSmemBytes = gemm_smem(GEMM_STAGES_SKINNY);
         cfg.stream = stream;
-        cudaLaunchAttribute at[1];
+        cudaLaunchAttribute at[2];
         at[0].id = cudaLaunchAttributeClusterDimension;
         at[0].val.clusterDim.x = 1; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = (unsigned)split;
-        cfg.attrs = at; cfg.numAttrs = 1;
+        at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = at; cfg.numAttrs = g_pdl_launch ? 2 : 1;
 #define Q35_GEMM_SKINNY(E)                                                                                                                       \
     case E: {                                                                                                                                    \
         static bool attr = false;                                                                                                                \

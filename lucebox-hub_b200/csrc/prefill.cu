@@ -82,24 +82,26 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
     for (int i = 0; i < FA_ROT / 2; ++i) rt.f[i] = 1.0f / (float)std::pow(1.0e7, (double)((float)(2 * i) / (float)FA_ROT));
 
     int i_dn = 0, i_fa = 0;
+    // ~250 dependent launches per prompt: programmatic dependent launch (every kernel of the pass starts with pdl_wait())
+    PdlGuard pdl_guard;
     for (int layer = 0; layer < a.n_layers; ++layer) {
         const LayerRec& L = a.layers_host[layer];
         const PrefillFused& F = a.fused_host[layer];
         // input norm (layer 0 gathers the embedding rows into `hidden` on the way)
-        pf_rmsnorm_kernel<<<S, 128, 0, stream>>>(layer == 0 ? a.token_ids : nullptr, a.embed, a.hidden, (const bf16*)L.p[0],
-                                                 layer == 0 ? a.hidden : nullptr, a.normalized, S);
+        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, S, 128, 0, stream, layer == 0 ? a.token_ids : nullptr, a.embed, a.hidden, (const bf16*)L.p[0],
+                                                 layer == 0 ? a.hidden : nullptr, a.normalized, S));
         g_launches.fetch_add(1);
         const bf16 *w_out, *w_post, *w_down;
         if (L.type == 0) {
             const int ldp = DN_PROJ_ROWS;
             Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)F.proj_weight, DN_PROJ_ROWS, a.proj_buf, ldp, nullptr, 0, S, DN_PROJ_ROWS, HIDDEN, 0, 0, stream));
-            pf_dn_prep_kernel<<<dim3(S, DN_HEADS), 128, 0, stream>>>(a.proj_buf, ldp, (const bf16*)L.p[DN_CONV], (const bf16*)L.p[DN_ALOG],
-                                                                      (const bf16*)L.p[DN_DTBIAS], a.proj_buf2, a.beta_buf, a.alpha_buf, S);
-            pf_conv_state_kernel<<<(DN_CONV_CH + 255) / 256, 256, 0, stream>>>(a.proj_buf, ldp, a.conv_bufs + (size_t)i_dn * DN_CONV_CH * 4, S);
-            pf_dn_chunk_local_kernel<<<dim3(nchunks, DN_HEADS), CL_THREADS, CHUNK_LOCAL_SMEM, stream>>>(a.proj_buf2, a.beta_buf, a.alpha_buf, scratch, S, nchunks);
-            pf_dn_chunk_scan_kernel<<<dim3(DN_HEADS, DN_V / SCAN_VW), SCAN_THREADS, CHUNK_SCAN_SMEM, stream>>>(
-                scratch, a.dn_out_buf, a.dn_states + (size_t)i_dn * DN_HEADS * DN_V * DN_K, S, nchunks);
-            pf_gated_norm_kernel<<<(S * DN_HEADS + 7) / 8, 256, 0, stream>>>(a.dn_out_buf, a.proj_buf, ldp, (const bf16*)L.p[DN_NORM], a.attn_buf, S);
+            Q35_CUDA_OK(pdl_launch(pf_dn_prep_kernel, dim3(S, DN_HEADS), 128, 0, stream, a.proj_buf, ldp, (const bf16*)L.p[DN_CONV], (const bf16*)L.p[DN_ALOG],
+                                                                      (const bf16*)L.p[DN_DTBIAS], a.proj_buf2, a.beta_buf, a.alpha_buf, S));
+            Q35_CUDA_OK(pdl_launch(pf_conv_state_kernel, (DN_CONV_CH + 255) / 256, 256, 0, stream, a.proj_buf, ldp, a.conv_bufs + (size_t)i_dn * DN_CONV_CH * 4, S));
+            Q35_CUDA_OK(pdl_launch(pf_dn_chunk_local_kernel, dim3(nchunks, DN_HEADS), CL_THREADS, CHUNK_LOCAL_SMEM, stream, a.proj_buf2, a.beta_buf, a.alpha_buf, scratch, S, nchunks));
+            Q35_CUDA_OK(pdl_launch(pf_dn_chunk_scan_kernel, dim3(DN_HEADS, DN_V / SCAN_VW), SCAN_THREADS, CHUNK_SCAN_SMEM, stream, 
+                scratch, a.dn_out_buf, a.dn_states + (size_t)i_dn * DN_HEADS * DN_V * DN_K, S, nchunks));
+            Q35_CUDA_OK(pdl_launch(pf_gated_norm_kernel, (S * DN_HEADS + 7) / 8, 256, 0, stream, a.dn_out_buf, a.proj_buf, ldp, (const bf16*)L.p[DN_NORM], a.attn_buf, S));
             g_launches.fetch_add(5);
             w_out = (const bf16*)L.p[DN_OUT]; w_post = (const bf16*)L.p[DN_POST_NORM]; w_down = (const bf16*)L.p[DN_DOWN];
             ++i_dn;
@@ -108,17 +110,17 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
             Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)F.proj_weight, FA_PROJ_ROWS, a.proj_buf, ldp, nullptr, 0, S, FA_PROJ_ROWS, HIDDEN, 0, 0, stream));
             bf16* kc = a.k_cache + (size_t)i_fa * FA_KV_HEADS * a.max_seq_len * FA_HEAD_DIM;
             bf16* vc = a.v_cache + (size_t)i_fa * FA_KV_HEADS * a.max_seq_len * FA_HEAD_DIM;
-            pf_qk_norm_rope_kernel<<<(S * 12 + 7) / 8, 256, 0, stream>>>(a.proj_buf, ldp, (const bf16*)L.p[FA_QNORM], (const bf16*)L.p[FA_KNORM], rt,
-                                                                         a.proj_buf2, kc, vc, S, a.max_seq_len);
-            pf_attention_mma_kernel<<<dim3((S + ATT_MMA_Q - 1) / ATT_MMA_Q, FA_KV_HEADS), 256, ATT_MMA_SMEM, stream>>>(
-                a.proj_buf2, kc, vc, a.proj_buf, ldp, a.attn_buf, S, a.max_seq_len);
+            Q35_CUDA_OK(pdl_launch(pf_qk_norm_rope_kernel, (S * 12 + 7) / 8, 256, 0, stream, a.proj_buf, ldp, (const bf16*)L.p[FA_QNORM], (const bf16*)L.p[FA_KNORM], rt,
+                                                                         a.proj_buf2, kc, vc, S, a.max_seq_len));
+            Q35_CUDA_OK(pdl_launch(pf_attention_mma_kernel, dim3((S + ATT_MMA_Q - 1) / ATT_MMA_Q, FA_KV_HEADS), 256, ATT_MMA_SMEM, stream, 
+                a.proj_buf2, kc, vc, a.proj_buf, ldp, a.attn_buf, S, a.max_seq_len));
             g_launches.fetch_add(2);
             w_out = (const bf16*)L.p[FA_O]; w_post = (const bf16*)L.p[FA_POST_NORM]; w_down = (const bf16*)L.p[FA_DOWN];
             ++i_fa;
         }
         // output projection + residual -> residual buffer holds the hidden state after the mixer
         Q35_TRY(gemm_bf16(a.attn_buf, 2048, w_out, HIDDEN, a.residual, HIDDEN, a.hidden, HIDDEN, S, HIDDEN, 2048, 1, 0, stream));
-        pf_rmsnorm_kernel<<<S, 128, 0, stream>>>(nullptr, nullptr, a.residual, w_post, nullptr, a.normalized, S);
+        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, S, 128, 0, stream, nullptr, nullptr, a.residual, w_post, nullptr, a.normalized, S));
         g_launches.fetch_add(1);
         Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)F.gate_up_weight, 2 * INTER, a.mlp_buf, INTER, nullptr, 0, S, INTER, HIDDEN, 2, INTER, stream));
         Q35_TRY(gemm_bf16(a.mlp_buf, INTER, w_down, HIDDEN, a.hidden, HIDDEN, a.residual, HIDDEN, S, HIDDEN, INTER, 1, 0, stream));
@@ -126,13 +128,13 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
     // last token: final norm, LM head, arg-max
     const bf16* last = a.hidden + (size_t)(S - 1) * HIDDEN;
     if (a.hidden_out) Q35_CUDA_OK(cudaMemcpyAsync(a.hidden_out, last, HIDDEN * sizeof(bf16), cudaMemcpyDeviceToDevice, stream));
-    pf_rmsnorm_kernel<<<1, 128, 0, stream>>>(nullptr, nullptr, last, a.final_norm, nullptr, a.final_normed, 1);
+    Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, 1, 128, 0, stream, nullptr, nullptr, last, a.final_norm, nullptr, a.final_normed, 1));
     const int lm_blocks = 592;
     if (a.lm_packed)
-        pf_lm_head_fp4_kernel<<<lm_blocks, 256, 0, stream>>>(a.final_normed, (const uint8_t*)a.lm_packed, (const uint8_t*)a.lm_scales, a.lm_bmv, a.lm_bmi, a.logits_out);
+        Q35_CUDA_OK(pdl_launch(pf_lm_head_fp4_kernel, lm_blocks, 256, 0, stream, a.final_normed, (const uint8_t*)a.lm_packed, (const uint8_t*)a.lm_scales, a.lm_bmv, a.lm_bmi, a.logits_out));
     else
-        pf_lm_head_kernel<<<lm_blocks, 256, 0, stream>>>(a.final_normed, a.lm_head, a.lm_bmv, a.lm_bmi, a.logits_out);
-    pf_lm_reduce_kernel<<<1, 32, 0, stream>>>(a.lm_bmv, a.lm_bmi, lm_blocks, a.out_token);
+        Q35_CUDA_OK(pdl_launch(pf_lm_head_kernel, lm_blocks, 256, 0, stream, a.final_normed, a.lm_head, a.lm_bmv, a.lm_bmi, a.logits_out));
+    Q35_CUDA_OK(pdl_launch(pf_lm_reduce_kernel, 1, 32, 0, stream, a.lm_bmv, a.lm_bmi, lm_blocks, a.out_token));
     g_launches.fetch_add(3);
     Q35_CUDA_OK(cudaGetLastError());
     return QWEN35_OK;

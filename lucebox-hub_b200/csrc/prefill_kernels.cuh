@@ -25,6 +25,7 @@ constexpr int DN_CHUNK = 64;
 static __global__ void __launch_bounds__(128) pf_rmsnorm_kernel(const int* __restrict__ ids, const bf16* __restrict__ embed,
                                                          const bf16* __restrict__ h_in, const bf16* __restrict__ w,
                                                          bf16* __restrict__ h_out, bf16* __restrict__ x_out, int S) {
+    pdl_wait();
     __shared__ float red[4];
     const int t = blockIdx.x, tid = threadIdx.x;
     const bf16* src = ids ? embed + (size_t)ids[t] * HIDDEN : h_in + (size_t)t * HIDDEN;
@@ -58,6 +59,7 @@ static __global__ void __launch_bounds__(128) pf_rmsnorm_kernel(const int* __res
 static __global__ void __launch_bounds__(128) pf_dn_prep_kernel(const bf16* __restrict__ proj, int ldp, const bf16* __restrict__ conv_w,
                                                          const bf16* __restrict__ a_log, const bf16* __restrict__ dt_bias,
                                                          bf16* __restrict__ qkv_out, float* __restrict__ beta, float* __restrict__ g, int S) {
+    pdl_wait();
     __shared__ float red[2][4];
     const int t = blockIdx.x, h = blockIdx.y, i = threadIdx.x;
     float c[3];
@@ -107,6 +109,7 @@ static __global__ void __launch_bounds__(128) pf_dn_prep_kernel(const bf16* __re
 
 // conv window after the prompt: the last four inputs per channel, zero-padded on the left, newest last
 static __global__ void pf_conv_state_kernel(const bf16* __restrict__ proj, int ldp, float* __restrict__ conv, int S) {
+    pdl_wait();
     const int ch = blockIdx.x * blockDim.x + threadIdx.x;
     if (ch >= DN_CONV_CH) return;
     float4 st;
@@ -144,6 +147,7 @@ __device__ __forceinline__ float dot4(const float4 a, const float4 b, float acc)
 static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(const bf16* __restrict__ qkv, const float* __restrict__ beta,
                                                                        const float* __restrict__ g, ChunkScratch* __restrict__ scratch,
                                                                        int S, int nchunks) {
+    pdl_wait();
     extern __shared__ __align__(16) float sm[];
     float* sq = sm;                                  // [64][CL_LD]  q / sqrt(128); later k * beta * exp(gc)
     float* sk = sq + DN_CHUNK * CL_LD;               // [64][CL_LD]  k
@@ -303,6 +307,7 @@ __device__ __forceinline__ void scan_cp16(float* dst, const float* src) {
 
 static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(const ChunkScratch* __restrict__ scratch, bf16* __restrict__ core_out,
                                                                         float* __restrict__ state_out, int S, int nchunks) {
+    pdl_wait();
     extern __shared__ __align__(16) float sm[];
     float* skcd = sm;                                   // [64][SCAN_LDK]
     float* sq = skcd + DN_CHUNK * SCAN_LDK;             // [64][SCAN_LDK]
@@ -430,6 +435,7 @@ static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(c
 // ---- gated RMSNorm of the DeltaNet output: one warp per (token, head) --------------------------------
 static __global__ void __launch_bounds__(256) pf_gated_norm_kernel(const bf16* __restrict__ core, const bf16* __restrict__ proj, int ldp,
                                                             const bf16* __restrict__ norm_w, bf16* __restrict__ out, int S) {
+    pdl_wait();
     const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (gw >= S * DN_HEADS) return;
     const int t = gw / DN_HEADS, h = gw % DN_HEADS;
@@ -457,6 +463,7 @@ static __global__ void __launch_bounds__(256) pf_qk_norm_rope_kernel(const bf16*
                                                               const bf16* __restrict__ kn_w, const RopeTable inv_freq,
                                                               bf16* __restrict__ q_out, bf16* __restrict__ k_cache, bf16* __restrict__ v_cache,
                                                               int S, int max_seq) {
+    pdl_wait();
     const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (gw >= S * 12) return;
     const int t = gw / 12, slot = gw % 12;
@@ -502,6 +509,7 @@ constexpr int ATT_MMA_SMEM = (ATT_MMA_ROWS + 2 * ATT_MMA_KEYS) * ATT_MMA_LD * 2;
 static __global__ void __launch_bounds__(256, 1) pf_attention_mma_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k_cache,
                                                                   const bf16* __restrict__ v_cache, const bf16* __restrict__ proj, int ldp,
                                                                   bf16* __restrict__ out, int S, int max_seq) {
+    pdl_wait();
     extern __shared__ __align__(16) unsigned char att_mma_sm[];
     bf16* Qs = reinterpret_cast<bf16*>(att_mma_sm);
     bf16* Ks = Qs + ATT_MMA_ROWS * ATT_MMA_LD;
@@ -633,6 +641,7 @@ static __global__ void __launch_bounds__(256, 1) pf_attention_mma_kernel(const b
 // ---- last-token LM head: GEMV over the vocabulary + arg-max (lowest index among equal bf16 maxima) -----
 static __global__ void __launch_bounds__(256) pf_lm_head_kernel(const bf16* __restrict__ x, const bf16* __restrict__ lm, float* __restrict__ bmv,
                                                          int* __restrict__ bmi, float* __restrict__ logits_out) {
+    pdl_wait();
     __shared__ float sv[8];
     __shared__ int si[8];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -675,6 +684,7 @@ static __global__ void __launch_bounds__(256) pf_lm_head_kernel(const bf16* __re
 static __global__ void __launch_bounds__(256) pf_lm_head_fp4_kernel(const bf16* __restrict__ x, const uint8_t* __restrict__ packed,
                                                              const uint8_t* __restrict__ scales, float* __restrict__ bmv, int* __restrict__ bmi,
                                                              float* __restrict__ logits_out) {
+    pdl_wait();
     __shared__ float sv[8];
     __shared__ int si[8];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -719,6 +729,7 @@ static __global__ void __launch_bounds__(256) pf_lm_head_fp4_kernel(const bf16* 
 }
 
 static __global__ void pf_lm_reduce_kernel(const float* __restrict__ bmv, const int* __restrict__ bmi, int n, int* __restrict__ out_token) {
+    pdl_wait();
     float bv = -INFINITY; int bi = 0x7fffffff;
     for (int i = threadIdx.x; i < n; i += 32) {
         const float v = bmv[i]; const int k = bmi[i];

@@ -33,4 +33,21 @@ extern bool g_pdl_launch;
         }                                                                         \
     } while (0)
 
+// launch with the programmatic-stream-serialization attribute: the kernel may be scheduled while its predecessor in the
+// stream drains.  Only for kernels that begin with pdl_wait() (common.cuh).  Also valid under stream capture.
+template <typename... KArgs, typename... Args>
+static inline cudaError_t pdl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid; cfg.blockDim = block; cfg.dynamicSmemBytes = smem; cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at; cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+struct PdlGuard {          // while alive, the GEMM launchers add the attribute too
+    PdlGuard() { g_pdl_launch = true; }
+    ~PdlGuard() { g_pdl_launch = false; }
+};
+
 }  // namespace q35

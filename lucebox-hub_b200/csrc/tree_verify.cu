@@ -728,20 +728,6 @@ struct TvScratch {
 
 static size_t align_up(size_t v) { return (v + 255) & ~(size_t)255; }
 
-// launch with the programmatic-stream-serialization attribute: the kernel may be scheduled while its predecessor in the
-// stream drains (every kernel launched this way starts with pdl_wait()).  Hides most of the 2-3 us between the ~660
-// dependent launches of a pass.
-template <typename... KArgs, typename... Args>
-static cudaError_t tv_launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args&&... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid; cfg.blockDim = block; cfg.dynamicSmemBytes = smem; cfg.stream = stream;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at; cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
-}
-
 static TvScratch tv_layout(const TvDims& D, int n, int max_ctx, char* base) {
     TvScratch s;
     size_t off = 0;
@@ -873,10 +859,11 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
         return QWEN35_ERR_BAD_ARG;
     }
 
-    struct PdlGuard { PdlGuard() { g_pdl_launch = true; } ~PdlGuard() { g_pdl_launch = false; } } pdl_guard;      // the Q4_K GEMM launches join in
-    Q35_CUDA_OK(tv_launch(tv_tree_prep_kernel, 1, 32, 0, stream, in->parents, n, s.depth, s.anc, s.dn_src, s.dn_save));
-    if (in->dense_mask & 1u) Q35_CUDA_OK(tv_launch(tv_embed_dense_kernel, n, 256, 0, stream, (const bf16*)in->token_embd, in->node_tokens, D.hidden, s.hidden));
-    else Q35_CUDA_OK(tv_launch(tv_embed_q4k_kernel, dim3(n, D.hidden / 256), 32, 0, stream, (const uint8_t*)in->token_embd, in->node_tokens, D.hidden, s.hidden));
+    // ~660 dependent launches per pass: programmatic dependent launch hides most of the 2-3 us between them
+    PdlGuard pdl_guard;      // the Q4_K GEMM launches join in
+    Q35_CUDA_OK(pdl_launch(tv_tree_prep_kernel, 1, 32, 0, stream, in->parents, n, s.depth, s.anc, s.dn_src, s.dn_save));
+    if (in->dense_mask & 1u) Q35_CUDA_OK(pdl_launch(tv_embed_dense_kernel, n, 256, 0, stream, (const bf16*)in->token_embd, in->node_tokens, D.hidden, s.hidden));
+    else Q35_CUDA_OK(pdl_launch(tv_embed_q4k_kernel, dim3(n, D.hidden / 256), 32, 0, stream, (const uint8_t*)in->token_embd, in->node_tokens, D.hidden, s.hidden));
     g_launches.fetch_add(2);
     const int n_layers = in->dbg_num_layers > 0 && in->dbg_num_layers < D.n_layers ? in->dbg_num_layers : D.n_layers;
     int i_fa = 0, i_dn = 0;
@@ -885,21 +872,21 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
         const bool is_fa = (il % D.fa_period) == D.fa_period - 1;
         if (il > 0 && in->dbg_teacher)
             Q35_CUDA_OK(cudaMemcpyAsync(s.hidden, (const bf16*)in->dbg_teacher + (size_t)il * n * D.hidden, (size_t)n * D.hidden * 2, cudaMemcpyDeviceToDevice, stream));
-        Q35_CUDA_OK(tv_launch(tv_rmsnorm_kernel, n, 256, 0, stream, s.hidden, (const float*)W.attn_norm, s.normed, D.hidden, D.eps));
+        Q35_CUDA_OK(pdl_launch(tv_rmsnorm_kernel, n, 256, 0, stream, s.hidden, (const float*)W.attn_norm, s.normed, D.hidden, D.eps));
         g_launches.fetch_add(1);
         int att_w;
         if (is_fa) {
             Q35_TRYT(q4k_linear(s.normed, D.hidden, W.w_in, (W.dense_mask & 1u) != 0, fa_in, D.hidden, s.proj, fa_in, nullptr, 0, n, 0, stream));
             unsigned char* kc = (unsigned char*)in->k_cache + (size_t)i_fa * kv_layer;
             unsigned char* vc = (unsigned char*)in->v_cache + (size_t)i_fa * kv_layer;
-            Q35_CUDA_OK(tv_launch(tv_fa_prep_kernel, dim3(n, D.q_heads + 2 * D.kv_heads), 128, 0, stream, s.proj, fa_in, (const float*)W.q_norm, (const float*)W.k_norm, s.depth, D,
+            Q35_CUDA_OK(pdl_launch(tv_fa_prep_kernel, dim3(n, D.q_heads + 2 * D.kv_heads), 128, 0, stream, s.proj, fa_in, (const float*)W.q_norm, (const float*)W.k_norm, s.depth, D,
                                                                                        in->past, in->max_ctx, s.qbuf, kc, vc, in->kv_type));
-            if (q8) Q35_CUDA_OK(tv_launch(tv_att_scores_kernel<true>, dim3(chunks, D.kv_heads), 256, sc_smem + q8_raw, stream, s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores));
-            else Q35_CUDA_OK(tv_launch(tv_att_scores_kernel<false>, dim3(chunks, D.kv_heads), 256, sc_smem, stream, s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores));
-            Q35_CUDA_OK(tv_launch(tv_att_stats_kernel, (D.kv_heads * R + 7) / 8, 256, 0, stream, s.scores, D.kv_heads * R, lpad, chunks * TV_CHUNK, s.stats));
-            if (q8) Q35_CUDA_OK(tv_launch(tv_att_pv_kernel<true>, dim3(chunks, D.kv_heads), 256, pv_smem + q8_raw, stream, vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial));
-            else Q35_CUDA_OK(tv_launch(tv_att_pv_kernel<false>, dim3(chunks, D.kv_heads), 256, pv_smem, stream, vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial));
-            Q35_CUDA_OK(tv_launch(tv_att_merge_kernel, dim3(n, D.q_heads), 128, 0, stream, s.partial, s.proj, fa_in, D, n, chunks, s.attn));
+            if (q8) Q35_CUDA_OK(pdl_launch(tv_att_scores_kernel<true>, dim3(chunks, D.kv_heads), 256, sc_smem + q8_raw, stream, s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores));
+            else Q35_CUDA_OK(pdl_launch(tv_att_scores_kernel<false>, dim3(chunks, D.kv_heads), 256, sc_smem, stream, s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores));
+            Q35_CUDA_OK(pdl_launch(tv_att_stats_kernel, (D.kv_heads * R + 7) / 8, 256, 0, stream, s.scores, D.kv_heads * R, lpad, chunks * TV_CHUNK, s.stats));
+            if (q8) Q35_CUDA_OK(pdl_launch(tv_att_pv_kernel<true>, dim3(chunks, D.kv_heads), 256, pv_smem + q8_raw, stream, vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial));
+            else Q35_CUDA_OK(pdl_launch(tv_att_pv_kernel<false>, dim3(chunks, D.kv_heads), 256, pv_smem, stream, vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial));
+            Q35_CUDA_OK(pdl_launch(tv_att_merge_kernel, dim3(n, D.q_heads), 128, 0, stream, s.partial, s.proj, fa_in, D, n, chunks, s.attn));
             g_launches.fetch_add(5);
             att_w = D.q_heads * TV_HD;
             ++i_fa;
@@ -914,17 +901,17 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
             float* nconv = (float*)in->node_conv + (size_t)i_dn * nconv_layer;
             __half* nstates = (__half*)in->node_states + (size_t)i_dn * nstate_layer;
             Q35_CUDA_OK(cudaStreamWaitEvent(stream, side.join, 0));
-            Q35_CUDA_OK(tv_launch(tv_dn_conv_norm_kernel, dim3(n, conv_ch / TV_DN), 128, 0, stream, s.proj, dn_in, in->parents, cstate, (const float*)W.conv_w, conv_ch, s.ba, 2 * D.dn_v_heads,
+            Q35_CUDA_OK(pdl_launch(tv_dn_conv_norm_kernel, dim3(n, conv_ch / TV_DN), 128, 0, stream, s.proj, dn_in, in->parents, cstate, (const float*)W.conv_w, conv_ch, s.ba, 2 * D.dn_v_heads,
                                                                               (const float*)W.ssm_a, (const float*)W.dt_bias, D, s.dn_qkv, nconv, s.dn_gate));
-            Q35_CUDA_OK(tv_launch(tv_dn_tree_kernel, dim3(D.dn_v_heads, TV_DN / 16), 128, tv_dn_tree_smem(n), stream, s.dn_qkv, conv_ch, s.dn_gate, in->parents, s.dn_src, s.dn_save, n, D,
+            Q35_CUDA_OK(pdl_launch(tv_dn_tree_kernel, dim3(D.dn_v_heads, TV_DN / 16), 128, tv_dn_tree_smem(n), stream, s.dn_qkv, conv_ch, s.dn_gate, in->parents, s.dn_src, s.dn_save, n, D,
                                                                                  (const float*)in->ssm_state + (size_t)i_dn * state_layer, nstates, s.core));
-            Q35_CUDA_OK(tv_launch(tv_dn_gated_norm_kernel, dim3(n, D.dn_v_heads), 128, 0, stream, s.core, s.proj, dn_in, z_off, (const float*)W.ssm_norm, D, s.attn));
+            Q35_CUDA_OK(pdl_launch(tv_dn_gated_norm_kernel, dim3(n, D.dn_v_heads), 128, 0, stream, s.core, s.proj, dn_in, z_off, (const float*)W.ssm_norm, D, s.attn));
             g_launches.fetch_add(3);
             att_w = D.dn_v_heads * TV_DN;
             ++i_dn;
         }
         Q35_TRYT(q4k_linear(s.attn, att_w, W.w_out, (W.dense_mask & 2u) != 0, D.hidden, att_w, s.resid, D.hidden, s.hidden, D.hidden, n, 1, stream));
-        Q35_CUDA_OK(tv_launch(tv_rmsnorm_kernel, n, 256, 0, stream, s.resid, (const float*)W.post_norm, s.normed, D.hidden, D.eps));
+        Q35_CUDA_OK(pdl_launch(tv_rmsnorm_kernel, n, 256, 0, stream, s.resid, (const float*)W.post_norm, s.normed, D.hidden, D.eps));
         g_launches.fetch_add(1);
         Q35_TRYT(q4k_linear(s.normed, D.hidden, W.w_gate_up, (W.dense_mask & 4u) != 0, D.ffn, D.hidden, s.mlp, D.ffn, nullptr, 0, n, 2, stream));
         Q35_TRYT(q4k_linear(s.mlp, D.ffn, W.w_down, (W.dense_mask & 8u) != 0, D.hidden, D.ffn, s.hidden, D.hidden, s.resid, D.hidden, n, 1, stream));
@@ -933,13 +920,13 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
         if (in->target_feat)
             for (int k = 0; k < in->n_capture; ++k)
                 if (in->capture_layers[k] == il) {
-                    Q35_CUDA_OK(tv_launch(tv_capture_kernel, n, 256, 0, stream, s.hidden, D.hidden, in->past, in->feat_cap, in->n_capture * D.hidden, k * D.hidden, (bf16*)in->target_feat));
+                    Q35_CUDA_OK(pdl_launch(tv_capture_kernel, n, 256, 0, stream, s.hidden, D.hidden, in->past, in->feat_cap, in->n_capture * D.hidden, k * D.hidden, (bf16*)in->target_feat));
                     g_launches.fetch_add(1);
                 }
     }
-    Q35_CUDA_OK(tv_launch(tv_rmsnorm_kernel, n, 256, 0, stream, s.hidden, (const float*)in->output_norm, s.normed, D.hidden, D.eps));
+    Q35_CUDA_OK(pdl_launch(tv_rmsnorm_kernel, n, 256, 0, stream, s.hidden, (const float*)in->output_norm, s.normed, D.hidden, D.eps));
     Q35_TRYT(q4k_linear(s.normed, D.hidden, in->output_w, (in->dense_mask & 2u) != 0, D.vocab, D.hidden, s.logits, D.vocab, nullptr, 0, n, 0, stream));
-    Q35_CUDA_OK(tv_launch(tv_argmax_kernel, n, 1024, 0, stream, s.logits, D.vocab, in->node_argmax));
+    Q35_CUDA_OK(pdl_launch(tv_argmax_kernel, n, 1024, 0, stream, s.logits, D.vocab, in->node_argmax));
     g_launches.fetch_add(2);
     if (in->logits_out) Q35_CUDA_OK(cudaMemcpyAsync(in->logits_out, s.logits, (size_t)n * D.vocab * 2, cudaMemcpyDeviceToDevice, stream));
     Q35_CUDA_OK(cudaGetLastError());
