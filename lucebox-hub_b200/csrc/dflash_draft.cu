@@ -52,6 +52,7 @@ __device__ __forceinline__ void dr_norm_rope_store(const bf16* __restrict__ src,
 // Q rows: grid (q_len, n_heads), 64 threads.  qraw [q_len][n_heads*128] -> qrot [q_len][n_heads][128], position ctx_len + row
 __global__ void __launch_bounds__(64) dr_q_prep_kernel(const bf16* __restrict__ qraw, const float* __restrict__ q_norm, int n_heads, int ctx_len,
                                                        float eps, float base, bf16* __restrict__ qrot) {
+    pdl_wait();
     __shared__ float red[2];
     const int r = blockIdx.x, h = blockIdx.y;
     const size_t off = ((size_t)r * n_heads + h) * DR_HD;
@@ -61,6 +62,7 @@ __global__ void __launch_bounds__(64) dr_q_prep_kernel(const bf16* __restrict__ 
 // K/V rows: grid (T, n_kv), 64 threads.  kv [T][2*n_kv*128] (k heads, then v heads) -> krot, vv [n_kv][T][128]; key row j sits at position j
 __global__ void __launch_bounds__(64) dr_kv_prep_kernel(const bf16* __restrict__ kv, const float* __restrict__ k_norm, int n_kv, int T, float eps,
                                                         float base, bf16* __restrict__ krot, bf16* __restrict__ vv) {
+    pdl_wait();
     __shared__ float red[2];
     const int j = blockIdx.x, h = blockIdx.y;
     const bf16* row = kv + (size_t)j * 2 * n_kv * DR_HD;
@@ -78,6 +80,7 @@ __global__ void __launch_bounds__(64) dr_kv_prep_kernel(const bf16* __restrict__
 __global__ void __launch_bounds__(128, 1) dr_attn_chunk_kernel(const bf16* __restrict__ qrot, const bf16* __restrict__ krot, const bf16* __restrict__ vv,
                                                                int n_heads, int n_kv, int q_len, int T, float scale, float* __restrict__ part,
                                                                float* __restrict__ ml) {
+    pdl_wait();
     extern __shared__ __align__(16) unsigned char dr_smem[];
     bf16* Qs = reinterpret_cast<bf16*>(dr_smem);              // [DR_ROWS][DR_LD]
     bf16* Ks = Qs + DR_ROWS * DR_LD;                          // [DR_CHUNK][DR_LD]
@@ -178,6 +181,7 @@ __global__ void __launch_bounds__(128, 1) dr_attn_chunk_kernel(const bf16* __res
 // out[q][head][d] = bf16( sum_c e^(m_c - M) part_c[d] / sum_c e^(m_c - M) l_c ), chunks in ascending order.  grid (q_len, n_heads), 128 threads
 __global__ void __launch_bounds__(128) dr_attn_merge_kernel(const float* __restrict__ part, const float* __restrict__ ml, int n_heads, int n_kv, int q_len,
                                                             int n_chunks, bf16* __restrict__ out) {
+    pdl_wait();
     const int qi = blockIdx.x, head = blockIdx.y, d = threadIdx.x;
     const int gqa = n_heads / n_kv, kvh = head / gqa, R = q_len * gqa, r = qi * gqa + head % gqa;
     float M = -INFINITY;
@@ -256,10 +260,11 @@ extern "C" int qwen35_b200_draft_forward(const Qwen35DraftArgs* in) {
         Q35_CUDA_OK(cudaFuncSetAttribute(dr_attn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)att_smem));
         attr_done = true;
     }
+    PdlGuard pdl_guard;      // every kernel of the forward starts with pdl_wait(): launches overlap their predecessor's drain
     // 1. feature fusion, once per call: target_feat = rms_norm(fc . target_hidden_cat) * hidden_norm -> rows 0..ctx-1 of X
     if (ctx > 0) {
         Q35_TRYD(gemm_bf16((const bf16*)in->target_hidden_cat, fc_in, (const bf16*)in->fc, H, s.feat_raw, H, nullptr, 0, ctx, H, fc_in, 0, 0, stream));
-        tv_rmsnorm_kernel<<<ctx, 256, 0, stream>>>(s.feat_raw, (const float*)in->hidden_norm, s.X, H, D.eps);
+        Q35_CUDA_OK(pdl_launch(tv_rmsnorm_kernel, ctx, 256, 0, stream, s.feat_raw, (const float*)in->hidden_norm, s.X, H, D.eps));
         g_launches.fetch_add(1);
     }
     Q35_CUDA_OK(cudaMemcpyAsync(s.h0, in->noise_embed, (size_t)q * H * 2, cudaMemcpyDeviceToDevice, stream));
@@ -272,22 +277,22 @@ extern "C" int qwen35_b200_draft_forward(const Qwen35DraftArgs* in) {
             set_error("draft_forward: layer %d has a null weight", il);
             return QWEN35_ERR_BAD_ARG;
         }
-        tv_rmsnorm_kernel<<<q, 256, 0, stream>>>(h, (const float*)L.attn_norm, hn, H, D.eps);
+        Q35_CUDA_OK(pdl_launch(tv_rmsnorm_kernel, q, 256, 0, stream, h, (const float*)L.attn_norm, hn, H, D.eps));
         Q35_TRYD(gemm_bf16(hn, H, (const bf16*)L.wq, qd, s.qraw, qd, nullptr, 0, q, qd, H, 0, 0, stream));
         Q35_TRYD(gemm_bf16(s.X, H, (const bf16*)L.wkv, 2 * kvd, s.kv, 2 * kvd, nullptr, 0, T, 2 * kvd, H, 0, 0, stream));
-        dr_q_prep_kernel<<<dim3(q, D.n_heads), 64, 0, stream>>>(s.qraw, (const float*)L.q_norm, D.n_heads, ctx, D.eps, D.rope_theta, s.qrot);
-        dr_kv_prep_kernel<<<dim3(T, D.n_kv_heads), 64, 0, stream>>>(s.kv, (const float*)L.k_norm, D.n_kv_heads, T, D.eps, D.rope_theta, s.krot, s.vv);
-        dr_attn_chunk_kernel<<<dim3(chunks, D.n_kv_heads), 128, att_smem, stream>>>(s.qrot, s.krot, s.vv, D.n_heads, D.n_kv_heads, q, T, scale, s.part, s.ml);
-        dr_attn_merge_kernel<<<dim3(q, D.n_heads), 128, 0, stream>>>(s.part, s.ml, D.n_heads, D.n_kv_heads, q, chunks, s.attn);
+        Q35_CUDA_OK(pdl_launch(dr_q_prep_kernel, dim3(q, D.n_heads), 64, 0, stream, s.qraw, (const float*)L.q_norm, D.n_heads, ctx, D.eps, D.rope_theta, s.qrot));
+        Q35_CUDA_OK(pdl_launch(dr_kv_prep_kernel, dim3(T, D.n_kv_heads), 64, 0, stream, s.kv, (const float*)L.k_norm, D.n_kv_heads, T, D.eps, D.rope_theta, s.krot, s.vv));
+        Q35_CUDA_OK(pdl_launch(dr_attn_chunk_kernel, dim3(chunks, D.n_kv_heads), 128, att_smem, stream, s.qrot, s.krot, s.vv, D.n_heads, D.n_kv_heads, q, T, scale, s.part, s.ml));
+        Q35_CUDA_OK(pdl_launch(dr_attn_merge_kernel, dim3(q, D.n_heads), 128, 0, stream, s.part, s.ml, D.n_heads, D.n_kv_heads, q, chunks, s.attn));
         Q35_TRYD(gemm_bf16(s.attn, qd, (const bf16*)L.wo, H, h_next, H, h, H, q, H, qd, 1, 0, stream));
         { bf16* t = h; h = h_next; h_next = t; }
-        tv_rmsnorm_kernel<<<q, 256, 0, stream>>>(h, (const float*)L.ffn_norm, s.hf, H, D.eps);
+        Q35_CUDA_OK(pdl_launch(tv_rmsnorm_kernel, q, 256, 0, stream, h, (const float*)L.ffn_norm, s.hf, H, D.eps));
         Q35_TRYD(gemm_bf16(s.hf, H, (const bf16*)L.w_gate_up, 2 * D.inter, s.mlp, D.inter, nullptr, 0, q, D.inter, H, 2, D.inter, stream));
         Q35_TRYD(gemm_bf16(s.mlp, D.inter, (const bf16*)L.w_down, H, h_next, H, h, H, q, H, D.inter, 1, 0, stream));
         { bf16* t = h; h = h_next; h_next = t; }
         g_launches.fetch_add(6);
     }
-    tv_rmsnorm_kernel<<<q, 256, 0, stream>>>(h, (const float*)in->out_norm, (bf16*)in->hidden_out, H, D.eps);
+    Q35_CUDA_OK(pdl_launch(tv_rmsnorm_kernel, q, 256, 0, stream, h, (const float*)in->out_norm, (bf16*)in->hidden_out, H, D.eps));
     g_launches.fetch_add(1);
     if (in->lm_head) {
         if (in->lm_head_q4k)
