@@ -202,6 +202,38 @@ def tree_verify_bench(dev, n_nodes=33, ctx=4096, iters=5, kv_type="bf16"):
             "roofline_frac": alg / (ms * 1e-3) / 1e9 / measured_peak()[0], "tflops": flops / (ms * 1e-3) / 1e12}
 
 
+def nvfp4_decode_bench(weights_gpu, dev, ids, n_gen, iters=3):
+    """the same architecture with NVFP4 weights (E2M1, 16-element blocks, E4M3 block scales, fp32 tensor
+    scale for the LM head; the reference pack layouts, packed by this library's own packers), bs=1, prompt 520, 128 greedy
+    tokens in one launch of the NVFP4 instantiation of the decode megakernel.  Prefill runs on the BF16 weights, as the
+    reference's prefill_bf16_nvfp4_lm does for the layer body."""
+    from qwen35_b200.model import Decoder
+    dec = Decoder(weights=weights_gpu, backend="nvfp4", max_seq_len=2048, device=dev)
+    first = dec.prefill_tokens(ids)
+    snap = [t.clone() for t in (dec._fa_k_cache, dec._fa_v_cache, dec._dn_states, dec._conv_bufs)]
+    pos = dec._position
+    times = []
+    for i in range(2 + iters):
+        for dst, src in zip((dec._fa_k_cache, dec._fa_v_cache, dec._dn_states, dec._conv_bufs), snap):
+            dst.copy_(src)
+        dec._position = pos
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        dec.step_many(first, n_gen)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        if i >= 2:
+            times.append(e0.elapsed_time(e1))
+    dec.check_status()
+    ms = min(times)
+    lc = pos + n_gen / 2.0
+    alg_per_tok = 751_304_704 * 0.5625 + 1_088_320 * 2 + 2048 + 37_748_736 + 3_538_944 + 12_288 * (lc + 1)
+    gbs = alg_per_tok * n_gen / (ms * 1e-3) / 1e9
+    return {"workload": "NVFP4 weights, bs=1, pp520 + tg128 greedy, one launch for the 128 tokens", "tg128_tok_s": n_gen / (ms * 1e-3),
+            "ms_per_token": ms / n_gen, "algorithmic_bytes_per_token": alg_per_tok, "hbm_gbs": gbs, "roofline_frac": gbs / measured_peak()[0],
+            "vs_bf16_note": "same latency chain as the BF16 kernel: the stage hand-offs, not the bytes, bound both"}
+
+
 def draft_forward_bench(dev, ctx=2048, iters=8):
     """Draft side of the speculative loop: the 5-layer DFlash draft at the reference's widths (hidden 5120, 32 / 8 heads of
     128, FFN 17408), bf16 random-init weights, a 2048-position feature window (the reference's cap) and 16 noise rows:
@@ -468,7 +500,12 @@ def run_ours(args):
     sweep = None
     if args.prefill_sweep and rank == 0:
         sweep = prefill_sweep(wg, dev, [int(x) for x in args.prefill_sweep.split(",")])
-    tree = draft = None
+    tree = draft = nvfp4 = None
+    if args.nvfp4 and rank == 0:
+        try:
+            nvfp4 = nvfp4_decode_bench(wg, dev, ids, GEN)
+        except Exception as exc:          # reported, never hidden: the section is additive to the bench line
+            nvfp4 = {"error": repr(exc)}
     if args.tree_verify and rank == 0:
         tree = tree_verify_bench(dev)
         tree["q8_0_kv_cache_ms"] = tree_verify_bench(dev, iters=3, kv_type="q8_0")["ms_per_verify_commit"]
@@ -536,6 +573,8 @@ def run_ours(args):
             line["tree_verify"] = tree
         if draft is not None:
             line["draft_forward"] = draft
+        if nvfp4 is not None:
+            line["nvfp4_decode"] = nvfp4
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(w_cpu, ids_cpu, 16, use_hf=False)
             if batched:
@@ -560,6 +599,7 @@ def main():
     ap.add_argument("--batched-groups", type=int, default=1, help="concurrent sub-batches of the batched-decode step (1 = one batch)")
     ap.add_argument("--kernel-table", action="store_true", help="print the per-kernel device times of one batched step to stderr")
     ap.add_argument("--prefill-sweep", default="128,512,1024,4096", help="prompt lengths of the prefill sweep ('' = skip)")
+    ap.add_argument("--nvfp4", type=int, default=1, help="run the NVFP4-weights decode section (0 = skip)")
     ap.add_argument("--only", choices=["draft_forward", "tree_verify"], default=None,
                     help="run just this section with --steps timed iterations and print its JSON (profiling aid; not the bench line)")
     ap.add_argument("--tree-verify", type=int, default=1, help="run the 27B-class tree-verify section (0 = skip)")
