@@ -270,7 +270,7 @@ def draft_forward_bench(dev, ctx=2048, iters=8):
             "hbm_frac": alg / (ms * 1e-3) / 1e9 / measured_peak()[0], "tflops": flops / (ms * 1e-3) / 1e12}
 
 
-def batched_decode_bench(weights_gpu, dev, rank, n_seq, ctx, n_steps, kernel_table=False, groups=1):
+def batched_decode_bench(weights_gpu, dev, rank, n_seq, ctx, n_steps, kernel_table=False, groups=1, graph=True):
     """Batched-decode configuration: `n_seq` independent sequences per GPU, `ctx`-token contexts prefilled by the library's own
     prefill, `n_steps` greedy steps.  Returns (tok/s on this rank, ms per step, algorithmic bytes per step)."""
     from qwen35_b200.config import QWEN35_0P8B as D
@@ -282,14 +282,14 @@ def batched_decode_bench(weights_gpu, dev, rank, n_seq, ctx, n_steps, kernel_tab
         bd.prefill(sq, make_token_ids(ctx, sequence_seed(0, rank, sq), D.vocab).to(dev))
     snap = [t.clone() for t in (bd.dn_states, bd.conv_bufs, bd.positions, bd.tokens)]
     for _ in range(3):
-        bd.step(graph=True)
+        bd.step(graph=graph)
     for dst, src in zip((bd.dn_states, bd.conv_bufs, bd.positions, bd.tokens), snap):
         dst.copy_(src)
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(n_steps):
-        bd.step(graph=True)
+        bd.step(graph=graph)
     e1.record()
     torch.cuda.synchronize(dev)
     bd.check_status()
@@ -513,7 +513,7 @@ def run_ours(args):
         draft = draft_forward_bench(dev)
     batched = None
     if args.batched > 0:
-        b_tok_s, b_ms, b_bytes = batched_decode_bench(wg, dev, rank, args.batched, args.batched_ctx, GEN, kernel_table=args.kernel_table and rank == 0, groups=args.batched_groups)
+        b_tok_s, b_ms, b_bytes = batched_decode_bench(wg, dev, rank, args.batched, args.batched_ctx, GEN, kernel_table=args.kernel_table and rank == 0, groups=args.batched_groups, graph=bool(args.batched_graph))
         from qwen35_b200.sharding import reduce_counters
         job = reduce_counters(tokens=args.batched * GEN, elapsed_ms=b_ms * GEN, algorithmic_bytes=b_bytes * GEN, device=dev)
         b_ms = job.elapsed_ms / GEN                         # slowest rank's time per step
@@ -599,6 +599,7 @@ def main():
     ap.add_argument("--batched-groups", type=int, default=1, help="concurrent sub-batches of the batched-decode step (1 = one batch)")
     ap.add_argument("--kernel-table", action="store_true", help="print the per-kernel device times of one batched step to stderr")
     ap.add_argument("--prefill-sweep", default="128,512,1024,4096", help="prompt lengths of the prefill sweep ('' = skip)")
+    ap.add_argument("--batched-graph", type=int, default=1, help="1: replay the batched step as a CUDA graph (default); 0: launch it eagerly")
     ap.add_argument("--nvfp4", type=int, default=1, help="run the NVFP4-weights decode section (0 = skip)")
     ap.add_argument("--only", choices=["draft_forward", "tree_verify"], default=None,
                     help="run just this section with --steps timed iterations and print its JSON (profiling aid; not the bench line)")
