@@ -155,11 +155,14 @@ def prefill_sweep(weights_gpu, dev, lengths):
     return out
 
 
-def tree_verify_bench(dev, n_nodes=33, ctx=4096, iters=5, kv_type="bf16"):
+def tree_verify_bench(dev, n_nodes=33, ctx=4096, iters=5, kv_type="bf16", n_layers=0):
     """Tree-verify configuration: 27B-class dims, Q4_K weights generated directly as random super-blocks (dequantised
     sigma ~0.02), a 4096-token context of random cache contents, one 33-node tree (seeded random parents, depth <= 8):
     milliseconds per verify + accept walk + commit, timed with CUDA events."""
     from qwen35_b200.tree_verify import QWEN35_27B as T, TreeTarget, make_random_tree_weights, random_tree
+    if n_layers:                      # a shallow model of the same widths: small enough for a multi-pass ncu capture
+        import dataclasses
+        T = dataclasses.replace(T, n_layers=n_layers)
     w = make_random_tree_weights(T, 11, device=dev)
     tt = TreeTarget(T, w, max_ctx=ctx + 128, device=dev, kv_type=kv_type)
     g = torch.Generator(device=dev).manual_seed(11)
@@ -411,8 +414,10 @@ def run_ours(args):
     if args.only:
         # one section alone (for profiling a path without the others' launches): prints that section's JSON, not the bench line
         if rank == 0:
-            fn = {"draft_forward": draft_forward_bench, "tree_verify": tree_verify_bench}[args.only]
-            print(json.dumps({args.only: fn(dev, iters=max(1, args.steps))}))
+            if args.only == "tree_verify":
+                print(json.dumps({args.only: tree_verify_bench(dev, iters=max(1, args.steps), n_layers=args.tree_layers)}))
+            else:
+                print(json.dumps({args.only: draft_forward_bench(dev, iters=max(1, args.steps))}))
         return
     if world > 1:
         import torch.distributed as dist
@@ -603,6 +608,7 @@ def main():
     ap.add_argument("--prefill-sweep", default="128,512,1024,4096", help="prompt lengths of the prefill sweep ('' = skip)")
     ap.add_argument("--batched-graph", type=int, default=1, help="1: replay the batched step as a CUDA graph (default); 0: launch it eagerly")
     ap.add_argument("--nvfp4", type=int, default=1, help="run the NVFP4-weights decode section (0 = skip)")
+    ap.add_argument("--tree-layers", type=int, default=0, help="with --only tree_verify: this many layers instead of 64 (same widths; profiling aid)")
     ap.add_argument("--only", choices=["draft_forward", "tree_verify"], default=None,
                     help="run just this section with --steps timed iterations and print its JSON (profiling aid; not the bench line)")
     ap.add_argument("--tree-verify", type=int, default=1, help="run the 27B-class tree-verify section (0 = skip)")

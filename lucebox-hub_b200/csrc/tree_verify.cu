@@ -293,43 +293,48 @@ __global__ void __launch_bounds__(256, 1) tv_att_scores_kernel(const bf16* __res
     __syncthreads();
     tv_finish_rows<Q8>(Ks, raw, j0, L, tid);
     const int g = lane >> 2, c = lane & 3;
-    for (int nt = warp; nt < TV_CHUNK / 8; nt += 8) {
-        uint32_t bfr[TV_HD / 16][2];
-        const bf16* kr = Ks + (size_t)(nt * 8 + g) * TV_QSTRIDE + 2 * c;
+    // warp w owns the 16 keys [16w, 16w + 16) of the chunk = two 8-key MMA tiles; their K fragments (ldmatrix) stay in
+    // registers for the whole kernel.  Query tiles go two at a time, so four independent accumulator chains are in
+    // flight (one chain of 16 dependent MMAs at a time left the tensor pipe waiting on its own latency).
+    static_assert(TV_CHUNK / 16 == 8, "one 16-key pair per warp");
+    uint32_t bfr[TV_HD / 16][4];
+#pragma unroll
+    for (int s = 0; s < TV_HD / 16; ++s)
+        ldsm_x4(bfr[s], Ks + (size_t)(warp * 16 + (lane & 7) + 8 * (lane >> 4)) * TV_QSTRIDE + s * 16 + 8 * ((lane >> 3) & 1));
+    auto emit = [&](const float (&acc)[4], int mt, int nt) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int r = mt * 16 + g + 8 * h;
+            if (r >= R) continue;
+            const unsigned long long am = anc[r / gqa];
+            float* dst = scores + ((size_t)kvh * R + r) * lpad + j0 + nt * 8 + 2 * c;
+            float2 out;
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int j = j0 + nt * 8 + 2 * c + e;
+                const bool vis = j < past || (j < L && ((am >> (j - past)) & 1ull));
+                (e ? out.y : out.x) = vis ? acc[2 * h + e] * 0.0625f : -INFINITY;
+            }
+            *reinterpret_cast<float2*>(dst) = out;
+        }
+    };
+    for (int mt = 0; mt < mt_n; mt += 2) {
+        const bool two = mt + 1 < mt_n;                       // block-uniform
+        float acc00[4] = {0.f, 0.f, 0.f, 0.f}, acc01[4] = {0.f, 0.f, 0.f, 0.f}, acc10[4] = {0.f, 0.f, 0.f, 0.f}, acc11[4] = {0.f, 0.f, 0.f, 0.f};
+        const bf16* qa = Qs + (size_t)(mt * 16 + (lane & 15)) * TV_QSTRIDE + (lane >> 4) * 8;
+        const bf16* qb = qa + (two ? 16 * TV_QSTRIDE : 0);
 #pragma unroll
         for (int s = 0; s < TV_HD / 16; ++s) {
-            bfr[s][0] = *reinterpret_cast<const uint32_t*>(kr + s * 16);
-            bfr[s][1] = *reinterpret_cast<const uint32_t*>(kr + s * 16 + 8);
+            uint32_t a0[4], a1[4];
+            ldsm_x4(a0, qa + s * 16);
+            ldsm_x4(a1, qb + s * 16);
+            mma_16816(acc00, a0, bfr[s][0], bfr[s][1]);
+            mma_16816(acc01, a0, bfr[s][2], bfr[s][3]);
+            mma_16816(acc10, a1, bfr[s][0], bfr[s][1]);
+            mma_16816(acc11, a1, bfr[s][2], bfr[s][3]);
         }
-        for (int mt = 0; mt < mt_n; ++mt) {
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            const bf16* q0 = Qs + (size_t)(mt * 16 + g) * TV_QSTRIDE + 2 * c;
-            const bf16* q1 = q0 + 8 * TV_QSTRIDE;
-#pragma unroll
-            for (int s = 0; s < TV_HD / 16; ++s) {
-                uint32_t a[4];
-                a[0] = *reinterpret_cast<const uint32_t*>(q0 + s * 16);
-                a[1] = *reinterpret_cast<const uint32_t*>(q1 + s * 16);
-                a[2] = *reinterpret_cast<const uint32_t*>(q0 + s * 16 + 8);
-                a[3] = *reinterpret_cast<const uint32_t*>(q1 + s * 16 + 8);
-                mma_16816(acc, a, bfr[s][0], bfr[s][1]);
-            }
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int r = mt * 16 + g + 8 * h;
-                if (r >= R) continue;
-                const unsigned long long am = anc[r / gqa];
-                float* dst = scores + ((size_t)kvh * R + r) * lpad + j0 + nt * 8 + 2 * c;
-                float2 out;
-#pragma unroll
-                for (int e = 0; e < 2; ++e) {
-                    const int j = j0 + nt * 8 + 2 * c + e;
-                    const bool vis = j < past || (j < L && ((am >> (j - past)) & 1ull));
-                    (e ? out.y : out.x) = vis ? acc[2 * h + e] * 0.0625f : -INFINITY;
-                }
-                *reinterpret_cast<float2*>(dst) = out;
-            }
-        }
+        emit(acc00, mt, 2 * warp); emit(acc01, mt, 2 * warp + 1);
+        if (two) { emit(acc10, mt + 1, 2 * warp); emit(acc11, mt + 1, 2 * warp + 1); }
     }
 }
 
@@ -375,7 +380,7 @@ __global__ void __launch_bounds__(256, 1) tv_att_pv_kernel(const unsigned char* 
     // P rows (overlapping the copies above): a warp takes one row at a time, a lane four consecutive keys, so the score
     // loads are 16-byte, coalesced and several rows deep in flight
     static_assert(TV_CHUNK == 128, "one warp covers a 128-key row with four keys per lane");
-#pragma unroll 4
+#pragma unroll 13
     for (int r = warp; r < mt_n * 16; r += 8) {
         float4 sc = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
         float m = 0.f, l = 1.f;
