@@ -151,6 +151,7 @@ __global__ void tv_tree_prep_kernel(const int* __restrict__ parents, int n, int*
 // 8 blocks of {f16 d, 32 x int8} = 272 bytes, quantised from the f32 values when a row is written
 // (d = amax / 127, q = roundf(x / d)) and read back as the bf16 operand bf16(d * q).
 constexpr int TV_Q8_ROW = (TV_HD / 32) * 34;
+constexpr int TV_PV_THREADS = 512;      // P.V kernel: 16 warps share the softmax arithmetic of a chunk (99 exp + divide per thread with 8)
 __host__ __device__ constexpr int tv_kv_row_bytes(int kv_type) { return kv_type ? TV_Q8_ROW : TV_HD * 2; }
 
 // one warp = one 32-element block: lane holds element `lane` of the block
@@ -165,14 +166,14 @@ __device__ __forceinline__ void tv_q8_store_block(unsigned char* blk, float v, i
 // stage 128 cache rows [j0, j0 + 128) of one kv head into the padded bf16 tile; rows >= L are zero.  bf16 rows are copied
 // straight into the tile; Q8_0 rows are copied raw into `raw` and converted by tv_finish_rows after the copies landed.
 template <bool Q8>
-__device__ __forceinline__ void tv_stage_rows(bf16* tile, unsigned char* raw, const unsigned char* head_base, int j0, int L, int tid) {
+__device__ __forceinline__ void tv_stage_rows(bf16* tile, unsigned char* raw, const unsigned char* head_base, int j0, int L, int tid, int nthr = 256) {
     if (Q8) {
-        for (int i = tid; i < TV_CHUNK * (TV_Q8_ROW / 16); i += 256) {
+        for (int i = tid; i < TV_CHUNK * (TV_Q8_ROW / 16); i += nthr) {
             const int k = i / (TV_Q8_ROW / 16), c = i % (TV_Q8_ROW / 16);
             if (j0 + k < L) cp_async16(raw + (size_t)k * TV_Q8_ROW + c * 16, head_base + (size_t)(j0 + k) * TV_Q8_ROW + c * 16);
         }
     } else {
-        for (int i = tid; i < TV_CHUNK * (TV_HD / 8); i += 256) {
+        for (int i = tid; i < TV_CHUNK * (TV_HD / 8); i += nthr) {
             const int k = i / (TV_HD / 8), c8 = i % (TV_HD / 8);
             bf16* dst = tile + (size_t)k * TV_QSTRIDE + c8 * 8;
             if (j0 + k < L) cp_async16(dst, head_base + ((size_t)(j0 + k) * TV_HD + c8 * 8) * 2);
@@ -182,9 +183,9 @@ __device__ __forceinline__ void tv_stage_rows(bf16* tile, unsigned char* raw, co
 }
 // call after cp_async_wait_all() + __syncthreads(); for Q8_0 converts the raw rows and synchronises again
 template <bool Q8>
-__device__ __forceinline__ void tv_finish_rows(bf16* tile, const unsigned char* raw, int j0, int L, int tid) {
+__device__ __forceinline__ void tv_finish_rows(bf16* tile, const unsigned char* raw, int j0, int L, int tid, int nthr = 256) {
     if (!Q8) return;
-    for (int i = tid; i < TV_CHUNK * (TV_HD / 32); i += 256) {
+    for (int i = tid; i < TV_CHUNK * (TV_HD / 32); i += nthr) {
         const int k = i / (TV_HD / 32), b = i % (TV_HD / 32);
         uint32_t o[16];
         if (j0 + k < L) {
@@ -366,7 +367,7 @@ __global__ void __launch_bounds__(256) tv_att_stats_kernel(const float* __restri
 // The V chunk is staged row-major by cp.async and read as the B operand with ldmatrix.trans; P goes to shared memory
 // row-major and is read as the A operand with ldmatrix.
 template <bool Q8>
-__global__ void __launch_bounds__(256, 1) tv_att_pv_kernel(const unsigned char* __restrict__ v_cache, const float* __restrict__ scores, const float* __restrict__ stats,
+__global__ void __launch_bounds__(TV_PV_THREADS, 1) tv_att_pv_kernel(const unsigned char* __restrict__ v_cache, const float* __restrict__ scores, const float* __restrict__ stats,
                                                            TvDims D, int n_nodes, int past, int max_ctx, int lpad, float* __restrict__ partial) {
     pdl_wait();
     extern __shared__ __align__(16) unsigned char tv_smem[];
@@ -376,12 +377,12 @@ __global__ void __launch_bounds__(256, 1) tv_att_pv_kernel(const unsigned char* 
     const int chunk = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int j0 = chunk * TV_CHUNK, L = past + n_nodes;
     unsigned char* raw = reinterpret_cast<unsigned char*>(Ps + (size_t)mt_n * 16 * TV_PSTRIDE);      // Q8_0 only
-    tv_stage_rows<Q8>(Vs, raw, v_cache + (size_t)kvh * max_ctx * tv_kv_row_bytes(Q8), j0, L, tid);
+    tv_stage_rows<Q8>(Vs, raw, v_cache + (size_t)kvh * max_ctx * tv_kv_row_bytes(Q8), j0, L, tid, TV_PV_THREADS);
     // P rows (overlapping the copies above): a warp takes one row at a time, a lane four consecutive keys, so the score
     // loads are 16-byte, coalesced and several rows deep in flight
     static_assert(TV_CHUNK == 128, "one warp covers a 128-key row with four keys per lane");
-#pragma unroll 13
-    for (int r = warp; r < mt_n * 16; r += 8) {
+#pragma unroll 7
+    for (int r = warp; r < mt_n * 16; r += TV_PV_THREADS / 32) {
         float4 sc = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
         float m = 0.f, l = 1.f;
         if (r < R) {
@@ -396,10 +397,10 @@ __global__ void __launch_bounds__(256, 1) tv_att_pv_kernel(const unsigned char* 
     }
     cp_async_wait_all();
     __syncthreads();
-    tv_finish_rows<Q8>(Vs, raw, j0, L, tid);
+    tv_finish_rows<Q8>(Vs, raw, j0, L, tid, TV_PV_THREADS);
     const int g = lane >> 2, c = lane & 3;
     const int n_chunks = gridDim.x;
-    for (int np = warp; np < TV_HD / 16; np += 8) {                   // pairs of 8-dim output tiles
+    for (int np = warp; np < TV_HD / 16; np += TV_PV_THREADS / 32) {                   // pairs of 8-dim output tiles
         uint32_t bfr[TV_CHUNK / 16][4];
 #pragma unroll
         for (int s = 0; s < TV_CHUNK / 16; ++s)
@@ -889,8 +890,8 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
             if (q8) Q35_CUDA_OK(pdl_launch(tv_att_scores_kernel<true>, dim3(chunks, D.kv_heads), 256, sc_smem + q8_raw, stream, s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores));
             else Q35_CUDA_OK(pdl_launch(tv_att_scores_kernel<false>, dim3(chunks, D.kv_heads), 256, sc_smem, stream, s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores));
             Q35_CUDA_OK(pdl_launch(tv_att_stats_kernel, (D.kv_heads * R + 7) / 8, 256, 0, stream, s.scores, D.kv_heads * R, lpad, chunks * TV_CHUNK, s.stats));
-            if (q8) Q35_CUDA_OK(pdl_launch(tv_att_pv_kernel<true>, dim3(chunks, D.kv_heads), 256, pv_smem + q8_raw, stream, vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial));
-            else Q35_CUDA_OK(pdl_launch(tv_att_pv_kernel<false>, dim3(chunks, D.kv_heads), 256, pv_smem, stream, vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial));
+            if (q8) Q35_CUDA_OK(pdl_launch(tv_att_pv_kernel<true>, dim3(chunks, D.kv_heads), TV_PV_THREADS, pv_smem + q8_raw, stream, vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial));
+            else Q35_CUDA_OK(pdl_launch(tv_att_pv_kernel<false>, dim3(chunks, D.kv_heads), TV_PV_THREADS, pv_smem, stream, vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial));
             Q35_CUDA_OK(pdl_launch(tv_att_merge_kernel, dim3(n, D.q_heads), 128, 0, stream, s.partial, s.proj, fa_in, D, n, chunks, s.attn));
             g_launches.fetch_add(5);
             att_w = D.q_heads * TV_HD;
