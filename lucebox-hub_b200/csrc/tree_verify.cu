@@ -151,7 +151,7 @@ __global__ void tv_tree_prep_kernel(const int* __restrict__ parents, int n, int*
 // 8 blocks of {f16 d, 32 x int8} = 272 bytes, quantised from the f32 values when a row is written
 // (d = amax / 127, q = roundf(x / d)) and read back as the bf16 operand bf16(d * q).
 constexpr int TV_Q8_ROW = (TV_HD / 32) * 34;
-constexpr int TV_PV_THREADS = 512;      // P.V kernel: 16 warps share the softmax arithmetic of a chunk (99 exp + divide per thread with 8)
+constexpr int TV_PV_THREADS = 512;      // scores and P.V kernels: 16 warps share a chunk (latency-bound with 8; P.V: 99 exp + divide per thread)
 __host__ __device__ constexpr int tv_kv_row_bytes(int kv_type) { return kv_type ? TV_Q8_ROW : TV_HD * 2; }
 
 // one warp = one 32-element block: lane holds element `lane` of the block
@@ -271,7 +271,7 @@ __global__ void __launch_bounds__(128) tv_fa_prep_kernel(const bf16* __restrict_
 // scores of all query rows of one kv head (row r = node * gqa + q-in-group) against one chunk of keys:
 // s = (q . k) / 16 in f32, masked to -inf outside [0, past) and the node's ancestors.  grid (chunks, kv_heads).
 template <bool Q8>
-__global__ void __launch_bounds__(256, 1) tv_att_scores_kernel(const bf16* __restrict__ qbuf, const unsigned char* __restrict__ k_cache,
+__global__ void __launch_bounds__(TV_PV_THREADS, 1) tv_att_scores_kernel(const bf16* __restrict__ qbuf, const unsigned char* __restrict__ k_cache,
                                                                const unsigned long long* __restrict__ anc, TvDims D, int n_nodes, int past,
                                                                int max_ctx, int lpad, float* __restrict__ scores) {
     pdl_wait();
@@ -282,26 +282,28 @@ __global__ void __launch_bounds__(256, 1) tv_att_scores_kernel(const bf16* __res
     const int chunk = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int j0 = chunk * TV_CHUNK, L = past + n_nodes;
     // Q rows and the K chunk go to shared memory by cp.async: every copy of the tile is in flight at once
-    for (int i = tid; i < mt_n * 16 * (TV_HD / 8); i += 256) {
+    for (int i = tid; i < mt_n * 16 * (TV_HD / 8); i += TV_PV_THREADS) {
         const int r = i / (TV_HD / 8), c8 = i % (TV_HD / 8);
         bf16* dst = Qs + (size_t)r * TV_QSTRIDE + c8 * 8;
         if (r < R) cp_async16(dst, qbuf + ((size_t)(r / gqa) * D.q_heads + kvh * gqa + r % gqa) * TV_HD + c8 * 8);
         else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
     }
     unsigned char* raw = reinterpret_cast<unsigned char*>(Ks + (size_t)TV_CHUNK * TV_QSTRIDE);      // Q8_0 only
-    tv_stage_rows<Q8>(Ks, raw, k_cache + (size_t)kvh * max_ctx * tv_kv_row_bytes(Q8), j0, L, tid);
+    tv_stage_rows<Q8>(Ks, raw, k_cache + (size_t)kvh * max_ctx * tv_kv_row_bytes(Q8), j0, L, tid, TV_PV_THREADS);
     cp_async_wait_all();
     __syncthreads();
-    tv_finish_rows<Q8>(Ks, raw, j0, L, tid);
+    tv_finish_rows<Q8>(Ks, raw, j0, L, tid, TV_PV_THREADS);
     const int g = lane >> 2, c = lane & 3;
-    // warp w owns the 16 keys [16w, 16w + 16) of the chunk = two 8-key MMA tiles; their K fragments (ldmatrix) stay in
-    // registers for the whole kernel.  Query tiles go two at a time, so four independent accumulator chains are in
-    // flight (one chain of 16 dependent MMAs at a time left the tensor pipe waiting on its own latency).
-    static_assert(TV_CHUNK / 16 == 8, "one 16-key pair per warp");
+    // 16 warps: warp w owns the 16 keys [16 kp, 16 kp + 16), kp = w mod 8, of the chunk = two 8-key MMA tiles (their K
+    // fragments, by ldmatrix, stay in registers for the whole kernel) and every other pair of query tiles (w / 8).  Query
+    // tiles go two at a time, so four independent accumulator chains are in flight (one chain of 16 dependent MMAs at a
+    // time left the tensor pipe waiting on its own latency).
+    static_assert(TV_CHUNK / 16 == 8 && TV_PV_THREADS == 512, "8 key pairs x 2 query-tile phases = 16 warps");
+    const int kp = warp & 7;
     uint32_t bfr[TV_HD / 16][4];
 #pragma unroll
     for (int s = 0; s < TV_HD / 16; ++s)
-        ldsm_x4(bfr[s], Ks + (size_t)(warp * 16 + (lane & 7) + 8 * (lane >> 4)) * TV_QSTRIDE + s * 16 + 8 * ((lane >> 3) & 1));
+        ldsm_x4(bfr[s], Ks + (size_t)(kp * 16 + (lane & 7) + 8 * (lane >> 4)) * TV_QSTRIDE + s * 16 + 8 * ((lane >> 3) & 1));
     auto emit = [&](const float (&acc)[4], int mt, int nt) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -319,8 +321,8 @@ __global__ void __launch_bounds__(256, 1) tv_att_scores_kernel(const bf16* __res
             *reinterpret_cast<float2*>(dst) = out;
         }
     };
-    for (int mt = 0; mt < mt_n; mt += 2) {
-        const bool two = mt + 1 < mt_n;                       // block-uniform
+    for (int mt = 2 * (warp >> 3); mt < mt_n; mt += 4) {
+        const bool two = mt + 1 < mt_n;                       // warp-uniform
         float acc00[4] = {0.f, 0.f, 0.f, 0.f}, acc01[4] = {0.f, 0.f, 0.f, 0.f}, acc10[4] = {0.f, 0.f, 0.f, 0.f}, acc11[4] = {0.f, 0.f, 0.f, 0.f};
         const bf16* qa = Qs + (size_t)(mt * 16 + (lane & 15)) * TV_QSTRIDE + (lane >> 4) * 8;
         const bf16* qb = qa + (two ? 16 * TV_QSTRIDE : 0);
@@ -334,8 +336,8 @@ __global__ void __launch_bounds__(256, 1) tv_att_scores_kernel(const bf16* __res
             mma_16816(acc10, a1, bfr[s][0], bfr[s][1]);
             mma_16816(acc11, a1, bfr[s][2], bfr[s][3]);
         }
-        emit(acc00, mt, 2 * warp); emit(acc01, mt, 2 * warp + 1);
-        if (two) { emit(acc10, mt + 1, 2 * warp); emit(acc11, mt + 1, 2 * warp + 1); }
+        emit(acc00, mt, 2 * kp); emit(acc01, mt, 2 * kp + 1);
+        if (two) { emit(acc10, mt + 1, 2 * kp); emit(acc11, mt + 1, 2 * kp + 1); }
     }
 }
 
@@ -887,8 +889,8 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
             unsigned char* vc = (unsigned char*)in->v_cache + (size_t)i_fa * kv_layer;
             Q35_CUDA_OK(pdl_launch(tv_fa_prep_kernel, dim3(n, D.q_heads + 2 * D.kv_heads), 128, 0, stream, s.proj, fa_in, (const float*)W.q_norm, (const float*)W.k_norm, s.depth, D,
                                                                                        in->past, in->max_ctx, s.qbuf, kc, vc, in->kv_type));
-            if (q8) Q35_CUDA_OK(pdl_launch(tv_att_scores_kernel<true>, dim3(chunks, D.kv_heads), 256, sc_smem + q8_raw, stream, s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores));
-            else Q35_CUDA_OK(pdl_launch(tv_att_scores_kernel<false>, dim3(chunks, D.kv_heads), 256, sc_smem, stream, s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores));
+            if (q8) Q35_CUDA_OK(pdl_launch(tv_att_scores_kernel<true>, dim3(chunks, D.kv_heads), TV_PV_THREADS, sc_smem + q8_raw, stream, s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores));
+            else Q35_CUDA_OK(pdl_launch(tv_att_scores_kernel<false>, dim3(chunks, D.kv_heads), TV_PV_THREADS, sc_smem, stream, s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores));
             Q35_CUDA_OK(pdl_launch(tv_att_stats_kernel, (D.kv_heads * R + 7) / 8, 256, 0, stream, s.scores, D.kv_heads * R, lpad, chunks * TV_CHUNK, s.stats));
             if (q8) Q35_CUDA_OK(pdl_launch(tv_att_pv_kernel<true>, dim3(chunks, D.kv_heads), TV_PV_THREADS, pv_smem + q8_raw, stream, vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial));
             else Q35_CUDA_OK(pdl_launch(tv_att_pv_kernel<false>, dim3(chunks, D.kv_heads), TV_PV_THREADS, pv_smem, stream, vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial));
