@@ -356,11 +356,11 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
 //   warp 1      MMA issue: 8 x (M128 N128 K16) per k-step once both operands of the stage are there
 //   warps 2-5   epilogue afterwards (park, cluster reduce, store) as in the bf16 kernel
 // The activation box holds 64 rows; the MMA reads 128, so accumulator rows 64-127 are garbage and are never read.
-// ncu on the gate/up shape (33 x 17408 x 5120): tensor pipe 10 % active, issue slots 61 % busy, 10 instructions per
-// weight: the kernel is bound by the dequantisation arithmetic, not by HBM (13 %) or the MMA.
+// ncu on a full wave of the gate/up widths (33 x 9472 x 5120): tensor pipe 33 % active, issue slots 47 % busy, 4.9
+// instructions per weight, HBM 19 %: the kernel is bound by the dequantisation arithmetic, not by HBM or the MMA.
 // The weight operand is value = fma_bf16(q, bf16(d*sc), -bf16(dmin*m)), two weights per instruction: the published f32
-// dequantisation (d*sc)*q - dmin*m followed by a rounding to bf16 costs ~10 instructions per weight on the CUDA cores
-// and bounded the kernel.  qwen35_b200_dequant_q4k keeps the published arithmetic bit for bit.  (An f16 weight
+// dequantisation (d*sc)*q - dmin*m followed by a rounding to bf16 cost ~10 instructions per weight on the CUDA cores
+// and bounded the kernel harder still.  qwen35_b200_dequant_q4k keeps the published arithmetic bit for bit.  (An f16 weight
 // operand beside bf16 activations is not an option: kind::f16 with different A and B formats raised "illegal
 // instruction" on this GPU.)
 constexpr int Q4K_THREADS = 608;                                                      // 2 + 16 dequantisation warps + the raw producer
