@@ -121,7 +121,22 @@ int launch_prefill_bf16_nvfp4_lm(
     void* final_normed, void* hidden_bf16_out, void* lm_bmv, void* lm_bmi,
     void* lm_hidden_bf16, void* lm_hidden_packed, void* lm_hidden_scales, void* lm_logits_f16, qwen35_stream_t stream);
 
-/* The same with an explicit cache length, optional logits and a layer limit for tests. */
+/* Replaces launch_prefill_bf16_mega (torch_bindings.cpp:354-364; prefill_megakernel.cu:840-1078), the reference's single-
+ * dispatch prompt pass: same inputs and results as launch_prefill_bf16 without the fused-weight table.  Each matrix of the
+ * layer records runs as its own tensor-core GEMM into the column blocks of proj_buf; SiLU(gate)*up is a kernel of its own
+ * (gate in proj_buf, up in proj_buf2).  Cache length 2048 (MAX_SEQ, prefill_megakernel.cu:37). */
+int launch_prefill_bf16_mega(
+    const int* token_ids, int seq_len, int* output_token,
+    const void* embed_weight, const LayerWeights* layers,
+    const void* final_norm_w, const void* lm_head_w,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* hidden, void* residual, void* normalized,
+    void* proj_buf, void* proj_buf2, void* attn_buf, void* mlp_buf,
+    void* dn_out_buf, void* beta_buf, void* alpha_buf,
+    void* final_normed, void* hidden_bf16_out, void* lm_bmv, void* lm_bmi, qwen35_stream_t stream);
+
+/* The same with an explicit cache length, optional logits and a layer limit for tests.  fused_layer_weights may be NULL:
+ * the pass then takes every matrix from layer_weights (the launch_prefill_bf16_mega form). */
 typedef struct {
     const int* token_ids; int seq_len; int* out_token;
     const void* embed_weight; const LayerWeights* layer_weights; const void* fused_layer_weights;
@@ -146,6 +161,8 @@ typedef struct {
     int dbg_num_layers;  /* 0 = all */
     const void* lm_head_weight_packed; /* optional: NVFP4 LM head (tensor-core layout) used for the last token */
     const void* lm_head_scales;
+    const void* dbg_teacher; /* optional bf16 [24][seq_len][1024]: layer l>0 reads row block l as its input (layer-level parity tests) */
+    void* dbg_hidden;        /* optional bf16 [24][1024]: every layer's output at the last position */
 } Qwen35PrefillArgs;
 int qwen35_b200_prefill_bf16(const Qwen35PrefillArgs* args, qwen35_stream_t stream);
 
@@ -176,6 +193,18 @@ int launch_decode_many_nvfp4(
     void* g_mlp_inter, void* g_z_scratch, void* g_beta_scratch, void* g_alpha_scratch, void* g_normalized,
     unsigned int* barrier_counter, unsigned int* barrier_generation, float* block_max_vals, int* block_max_idxs,
     unsigned int* lm_sync_counter, int position, int max_seq_len, int group_size, qwen35_stream_t stream);
+/* Replaces launch_prefill_megakernel_nvfp4 (torch_bindings.cpp:104-119; kernel_gb10_nvfp4.cu:1659-1755, 2119-2183): the
+ * single-dispatch prompt pass of the NVFP4 path.  Token-serial like the reference's: the decode megakernel runs the seq_len
+ * prompt tokens from position 0 in one launch, the LM head after the last; output_token_id[0] = the first generated token. */
+int launch_prefill_megakernel_nvfp4(
+    const int* token_ids, int seq_len, int* output_token_id, const void* embed_weight, const void* layer_weights,
+    const void* final_norm_weight, const void* lm_head_weight_packed, const void* lm_head_scales,
+    void* lm_hidden_bf16, void* lm_hidden_packed, void* lm_hidden_scales, void* lm_logits_f16,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs, void* hidden_buffer,
+    void* g_activations, void* g_residual, void* g_qkv_scratch, void* g_kv_scratch, void* g_attn_out,
+    void* g_mlp_inter, void* g_z_scratch, void* g_beta_scratch, void* g_alpha_scratch, void* g_normalized,
+    unsigned int* barrier_counter, unsigned int* barrier_generation, float* block_max_vals, int* block_max_idxs,
+    unsigned int* lm_sync_counter, int max_seq_len, int group_size, qwen35_stream_t stream);
 /* qwen35_b200_decode_steps for the NVFP4 format (logits, teacher forcing, debug outputs). */
 int qwen35_b200_decode_steps_nvfp4(const Qwen35DecodeArgs* args, const void* lm_head_scales, qwen35_stream_t stream);
 
@@ -379,7 +408,7 @@ int qwen35_b200_gemm_bf16(const void* A, int lda, const void* B, int b_rows, voi
                           int M, int N, int K, int epilogue, int up_row_offset, qwen35_stream_t stream);
 
 /* The same contraction with Q4_K weights (W = super-blocks [w_rows][K/256][144]), dequantised inside the kernel
- * (the role of ggml_mul_mat on a K-quant tensor, qwen35_target_graph.cpp:262-273, 295-404, 438-661).  M <= 128,
+ * (the role of ggml_mul_mat on a K-quant tensor, qwen35_target_graph.cpp:262-273, 295-404, 438-661).  M <= 64,
  * K a multiple of 256; rows of W beyond w_rows read as zero. */
 int qwen35_b200_gemm_q4k(const void* A, int lda, const void* W, int w_rows, void* C, int ldc, const void* R, int ldr,
                          int M, int N, int K, int epilogue, int up_row_offset, qwen35_stream_t stream);
@@ -406,6 +435,10 @@ int qwen35_b200_decode_steps_static(const Qwen35DecodeArgs* args, qwen35_stream_
  * library after an error. */
 int qwen35_b200_status(qwen35_stream_t stream);
 int qwen35_b200_clear_status(qwen35_stream_t stream);
+/* Both read / clear only the status words that exist already: neither creates the library workspace, so a process that
+ * uses only qwen35_b200_decode_steps_static never allocates through them.  qwen35_b200_workspace_if_any() returns the
+ * workspace of the current device, or NULL while no call has created it (a test hook for exactly that property). */
+const void* qwen35_b200_workspace_if_any(void);
 
 /* Debug: synchronise the device and copy one inter-stage vector of the workspace to the host.
  * which: 0 = stage-A output (8224 bf16), 1 = DeltaNet core output (2048 bf16), 2 = hidden after the

@@ -46,6 +46,16 @@ struct LayerRec {
 };
 static_assert(sizeof(LayerRec) == 128, "layer record is 128 bytes");
 
+// Fused prefill weights of one layer (reference: struct PrefillFusedLayerWeights, torch_bindings.cpp:31-38, prefill.cu:66-73).
+struct PrefillFused {
+    const void* proj_weight;     // DN: [qkv; z; b; a] = 8224 x 1024, FA: [q; k; v] = 5120 x 1024
+    const void* gate_up_weight;  // [gate; up] = 7168 x 1024
+    const void* unused[4];       // NVFP4 copies of the same matrices (not read by the BF16 path)
+};
+// Host copies of the two device tables, cached per pair of device addresses by the prefill launcher.
+struct HostTables { const void* dev_layers; const void* dev_fused; LayerRec layers[NUM_LAYERS]; PrefillFused fused[NUM_LAYERS]; };
+bool host_layer_tables(const void* dev_layers, const void* dev_fused, HostTables* out);
+
 // Pointer slots (models/qwen35_0p8b/model.py:342-380).
 enum FaSlot { FA_IN_NORM = 0, FA_Q, FA_K, FA_V, FA_QNORM, FA_KNORM, FA_O, FA_POST_NORM, FA_GATE, FA_UP, FA_DOWN };
 enum DnSlot { DN_IN_NORM = 0, DN_QKV, DN_Z, DN_B, DN_A, DN_CONV, DN_ALOG, DN_DTBIAS, DN_NORM, DN_OUT, DN_POST_NORM,

@@ -111,6 +111,8 @@ __global__ void bd_conv_shift_kernel(const bf16* __restrict__ proj, int ldp, flo
     *p = make_float4(s.y, s.z, s.w, bf2f(proj[(size_t)b * ldp + ch]));
 }
 
+__device__ __forceinline__ bool bd_pos_ok(int pos, int max_ctx) { return pos >= 0 && pos < max_ctx; }
+
 __device__ __forceinline__ bf16* kv_row(bf16* pages, const int* table, int max_pages, int b, int kvh, int pos) {
     const int page = table[b * max_pages + pos / KV_PAGE];
     return pages + (((size_t)page * FA_KV_HEADS + kvh) * KV_PAGE + (pos % KV_PAGE)) * FA_HEAD_DIM;
@@ -120,11 +122,19 @@ __device__ __forceinline__ bf16* kv_row(bf16* pages, const int* table, int max_p
 __global__ void __launch_bounds__(256) bd_qk_norm_rope_kernel(const bf16* __restrict__ proj, int ldp, const bf16* __restrict__ qn_w,
                                                               const bf16* __restrict__ kn_w, const RopeTable inv_freq,
                                                               const int* __restrict__ positions, const int* __restrict__ table, int max_pages,
-                                                              bf16* __restrict__ q_out, bf16* __restrict__ k_pages, bf16* __restrict__ v_pages, int B) {
+                                                              bf16* __restrict__ q_out, bf16* __restrict__ k_pages, bf16* __restrict__ v_pages, int B,
+                                                              int max_ctx, int* __restrict__ err) {
     pdl_wait();
     const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (gw >= B * 12) return;
     const int b = gw / 12, slot = gw % 12, pos = positions[b];
+    // A sequence whose position left [0, max_ctx) would index the block table beyond its row and the score scratch beyond
+    // max_ctx.  Positions advance on the device, so the check is here: the row is skipped (no K/V write, its attention
+    // output is zero, its position stops advancing) and the sticky status word reports a bad argument.
+    if (!bd_pos_ok(pos, max_ctx)) {
+        if (lane == 0 && slot == 0) atomicCAS(err, 0, (int)ERR_BAD_ARG);
+        return;
+    }
     if (slot >= 10) {
         const int kvh = slot - 10;
         const uint4 v = *(reinterpret_cast<const uint4*>(proj + (size_t)b * ldp + FA_QPROJ + FA_KV_SIZE + kvh * FA_HEAD_DIM) + lane);
@@ -204,7 +214,7 @@ __global__ void __launch_bounds__(128) bd_att_scores_kernel(const bf16* __restri
     bf16* Ks = Qs + 16 * BD_LD;                          // [BD_CHUNK][BD_LD]
     const int b = blockIdx.x, kvh = blockIdx.y, c = blockIdx.z, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int L = positions[b] + 1, j0 = c * BD_CHUNK;
-    if (j0 >= L) return;
+    if (!bd_pos_ok(L - 1, max_ctx) || j0 >= L) return;
     const int j1 = min(L, j0 + BD_CHUNK), cn = j1 - j0;
     const int* tb = table + b * max_pages;
     for (int i = tid; i < 16 * (FA_HEAD_DIM / 8); i += 128) {
@@ -270,7 +280,7 @@ __global__ void __launch_bounds__(128) bd_att_pv_kernel(const bf16* __restrict__
     bf16* Ps = Vs + BD_CHUNK * BD_LD;                    // [16][BD_PLD], rows 0-3 = P of the four heads
     const int b = blockIdx.x, kvh = blockIdx.y, c = blockIdx.z, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int L = positions[b] + 1, j0 = c * BD_CHUNK;
-    if (j0 >= L) return;
+    if (!bd_pos_ok(L - 1, max_ctx) || j0 >= L) return;
     const int j1 = min(L, j0 + BD_CHUNK), cn = j1 - j0;
     const int nch = (L + BD_CHUNK - 1) / BD_CHUNK;
     const int* tb = table + b * max_pages;
@@ -319,11 +329,16 @@ __global__ void __launch_bounds__(128) bd_att_pv_kernel(const bf16* __restrict__
 }
 
 __global__ void __launch_bounds__(256) bd_att_merge_kernel(const float* __restrict__ partial, const int* __restrict__ positions,
-                                                           const bf16* __restrict__ proj, int ldp, bf16* __restrict__ out, int B, int max_chunks) {
+                                                           const bf16* __restrict__ proj, int ldp, bf16* __restrict__ out, int B, int max_chunks,
+                                                           int max_ctx) {
     pdl_wait();
     const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (gw >= B * FA_Q_HEADS) return;
     const int b = gw / FA_Q_HEADS, head = gw % FA_Q_HEADS;
+    if (!bd_pos_ok(positions[b], max_ctx)) {           // skipped sequence: a defined (zero) attention output
+        *(reinterpret_cast<uint4*>(out + (size_t)b * FA_Q_SIZE + head * FA_HEAD_DIM) + lane) = make_uint4(0, 0, 0, 0);
+        return;
+    }
     const int nch = (positions[b] + 1 + BD_CHUNK - 1) / BD_CHUNK;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     const float* pb = partial + ((size_t)b * FA_Q_HEADS + head) * max_chunks * FA_HEAD_DIM + lane * 8;
@@ -344,7 +359,7 @@ __global__ void __launch_bounds__(256) bd_att_merge_kernel(const float* __restri
 }
 
 // ---- per-row arg-max over bf16 logits [B, VOCAB]: one CTA per row ---------------------------------------
-__global__ void __launch_bounds__(1024) bd_argmax_kernel(const bf16* __restrict__ logits, int* __restrict__ out_tokens, int* __restrict__ positions) {
+__global__ void __launch_bounds__(1024) bd_argmax_kernel(const bf16* __restrict__ logits, int* __restrict__ out_tokens, int* __restrict__ positions, int max_ctx) {
     pdl_wait();
     __shared__ float sv[32];
     __shared__ int si[32];
@@ -372,7 +387,8 @@ __global__ void __launch_bounds__(1024) bd_argmax_kernel(const bf16* __restrict_
             const float v = __shfl_xor_sync(0xffffffffu, best, o); const int k = __shfl_xor_sync(0xffffffffu, best_i, o);
             if (v > best || (v == best && k < best_i)) { best = v; best_i = k; }
         }
-        if (tid == 0) { out_tokens[b] = best_i; if (positions) positions[b] += 1; }
+        // a sequence that is already outside [0, max_ctx) was skipped by this step and stays where it is
+        if (tid == 0) { out_tokens[b] = best_i; if (positions && bd_pos_ok(positions[b], max_ctx)) positions[b] += 1; }
     }
 }
 
@@ -400,8 +416,7 @@ static void* batched_scratch(size_t bytes) {
     return g_bscratch[dev];
 }
 
-struct PrefillFusedB { const void* proj_weight; const void* gate_up_weight; const void* unused[4]; };
-const void* host_layer_tables(const void* dev_layers, const void* dev_fused, const void** fused_out);
+typedef PrefillFused PrefillFusedB;
 
 }  // namespace q35
 
@@ -443,17 +458,18 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
     // (read back once per pair of table pointers, as for prefill)
     const LayerRec* layers_h = reinterpret_cast<const LayerRec*>(in->layer_weights_host);
     const PrefillFusedB* fused_h = reinterpret_cast<const PrefillFusedB*>(in->fused_layer_weights_host);
+    HostTables tables;           // this call's own copy: a concurrent forget / eviction cannot pull it away
     if (!layers_h || !fused_h) {
-        const void* f = nullptr;
-        layers_h = reinterpret_cast<const LayerRec*>(host_layer_tables(in->layer_weights, in->fused_layer_weights, &f));
-        fused_h = reinterpret_cast<const PrefillFusedB*>(f);
-        if (!layers_h) return QWEN35_ERR_CUDA;
+        if (!in->layer_weights || !in->fused_layer_weights) { set_error("batched decode: null layer tables"); return QWEN35_ERR_BAD_ARG; }
+        if (!host_layer_tables(in->layer_weights, in->fused_layer_weights, &tables)) return QWEN35_ERR_CUDA;
+        layers_h = tables.layers;
+        fused_h = tables.fused;
     }
-    static bool attr_done = false;
-    if (!attr_done) {
+    static PerDeviceOnce attr_done;
+    if (attr_done.pending()) {
         Q35_CUDA_OK(cudaFuncSetAttribute(bd_att_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BD_SC_SMEM));
         Q35_CUDA_OK(cudaFuncSetAttribute(bd_att_pv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BD_PV_SMEM));
-        attr_done = true;
+        attr_done.mark();
     }
     // scratch rows of B tokens
     const size_t rows = (size_t)B;
@@ -473,6 +489,8 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
         base = (char*)batched_scratch(total);
         if (!base) return QWEN35_ERR_CUDA;
     }
+    int* status_word = (int*)get_workspace();      // the sticky device status word qwen35_b200_status() reads (the GEMMs use it too)
+    if (!status_word) return QWEN35_ERR_CUDA;
     bf16* hidden = (bf16*)base;
     bf16* resid = hidden + n_hidden;
     bf16* normed = resid + n_hidden;
@@ -521,11 +539,11 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
             bf16* kp = (bf16*)in->k_pages + (size_t)i_fa * page_layer_stride;
             bf16* vp = (bf16*)in->v_pages + (size_t)i_fa * page_layer_stride;
             Q35_CUDA_OK(pdl_launch(bd_qk_norm_rope_kernel, (B * 12 + 7) / 8, 256, 0, stream, proj, ldp, (const bf16*)L.p[FA_QNORM], (const bf16*)L.p[FA_KNORM], rt,
-                                                                         in->positions, in->block_table, in->max_pages, qbuf, kp, vp, B));
+                                                                         in->positions, in->block_table, in->max_pages, qbuf, kp, vp, B, in->max_ctx, status_word));
             const dim3 agrid(B, FA_KV_HEADS, max_chunks);
             Q35_CUDA_OK(pdl_launch(bd_att_scores_kernel, agrid, 128, BD_SC_SMEM, stream, qbuf, kp, in->positions, in->block_table, in->max_pages, att_scores, att_stats, in->max_ctx, max_chunks));
             Q35_CUDA_OK(pdl_launch(bd_att_pv_kernel, agrid, 128, BD_PV_SMEM, stream, vp, in->positions, in->block_table, in->max_pages, att_scores, att_stats, att_part, in->max_ctx, max_chunks));
-            Q35_CUDA_OK(pdl_launch(bd_att_merge_kernel, (B * FA_Q_HEADS + 7) / 8, 256, 0, stream, att_part, in->positions, proj, ldp, attn, B, max_chunks));
+            Q35_CUDA_OK(pdl_launch(bd_att_merge_kernel, (B * FA_Q_HEADS + 7) / 8, 256, 0, stream, att_part, in->positions, proj, ldp, attn, B, max_chunks, in->max_ctx));
             g_launches.fetch_add(4);
             w_out = (const bf16*)L.p[FA_O]; w_post = (const bf16*)L.p[FA_POST_NORM]; w_down = (const bf16*)L.p[FA_DOWN];
             ++i_fa;
@@ -540,7 +558,7 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
     }
     Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, B, 128, 0, stream, nullptr, nullptr, hidden, (const bf16*)in->final_norm_weight, nullptr, normed, B));
     Q35_TRYB(gemm_bf16(normed, HIDDEN, (const bf16*)in->lm_head_weight, VOCAB, logits, VOCAB, nullptr, 0, B, VOCAB, HIDDEN, 0, 0, stream));
-    Q35_CUDA_OK(pdl_launch(bd_argmax_kernel, B, 1024, 0, stream, logits, in->tokens_out, in->advance_positions ? in->positions : nullptr));
+    Q35_CUDA_OK(pdl_launch(bd_argmax_kernel, B, 1024, 0, stream, logits, in->tokens_out, in->advance_positions ? in->positions : nullptr, in->max_ctx));
     if (in->logits_out) Q35_CUDA_OK(cudaMemcpyAsync(in->logits_out, logits, n_logits * sizeof(bf16), cudaMemcpyDeviceToDevice, stream));
     g_launches.fetch_add(2);
     Q35_CUDA_OK(cudaGetLastError());

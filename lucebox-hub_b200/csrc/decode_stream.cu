@@ -1092,6 +1092,12 @@ static int launch_decode_impl(const DecodeArgs& in, cudaStream_t stream, bool us
         const int cap = (g / FA_KV_HEADS < ATT_MAX_CHUNKS ? g / FA_KV_HEADS : ATT_MAX_CHUNKS) * ATT_CHUNK_MAX;
         if (a.max_seq_len > cap) { set_error("max_seq_len %d exceeds %d on this device", a.max_seq_len, cap); return QWEN35_ERR_BAD_ARG; }
     }
+    if (fp4 && !a.lm_scales) { set_error("NVFP4 decode needs the LM-head scales"); return QWEN35_ERR_BAD_ARG; }
+    // The epoch counters and the static array's address are shared by every host thread that calls in on this
+    // device: one lock covers the look-up, the epoch range hand-out and the launch, so ranges never overlap and
+    // launches enter the stream in epoch order.
+    static std::mutex launch_mu;
+    std::lock_guard<std::mutex> lk(launch_mu);
     unsigned* epoch = use_static ? &g_static_epoch[dev] : &g_epoch[dev];
     if (use_static) {
         if (!g_static_ptr[dev]) {
@@ -1115,11 +1121,10 @@ static int launch_decode_impl(const DecodeArgs& in, cudaStream_t stream, bool us
     }
     a.epoch_base = *epoch;
     a.tma_period = tma_period();
-    *epoch += (unsigned)(32u * (unsigned)a.n_steps);
     void* params[] = {(void*)&a};
-    if (fp4 && !a.lm_scales) { set_error("NVFP4 decode needs the LM-head scales"); return QWEN35_ERR_BAD_ARG; }
     const void* kern = fp4 ? (const void*)decode_stream_kernel<true> : (const void*)decode_stream_kernel<false>;
     Q35_CUDA_OK(cudaLaunchCooperativeKernel(kern, dim3(decode_grid()), dim3(STREAM_THREADS), params, sizeof(Smem), stream));
+    *epoch += (unsigned)(32u * (unsigned)a.n_steps);      // only a launch that went out consumes its epoch range
     g_launches.fetch_add(1);
     return QWEN35_OK;
 }
@@ -1240,6 +1245,28 @@ extern "C" int launch_decode_many_nvfp4(
     // token_buffer[0] holds the first input token and receives the last generated one, as in the reference
     return nvfp4_common(token_buffer, token_buffer, output_tokens, steps, embed_weight, layer_weights, final_norm_weight, lm_head_weight_packed,
                         lm_head_scales, fa_k_cache, fa_v_cache, dn_states, conv_bufs, hidden_buffer, position, max_seq_len, group_size, stream);
+}
+
+// Replaces launch_prefill_megakernel_nvfp4 (torch_bindings.cpp:104-119; prefill_kernel_nvfp4, kernel_gb10_nvfp4.cu:1659-1755,
+// launcher :2119-2183): the prompt pass of the NVFP4 path, token-serial in the reference as well -- the decode megakernel is
+// run over the seq_len prompt tokens from position 0 in one launch and the LM head only after the last one.
+extern "C" int launch_prefill_megakernel_nvfp4(
+    const int* token_ids, int seq_len, int* output_token_id, const void* embed_weight, const void* layer_weights,
+    const void* final_norm_weight, const void* lm_head_weight_packed, const void* lm_head_scales,
+    void*, void*, void*, void*,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs, void* hidden_buffer,
+    void*, void*, void*, void*, void*, void*, void*, void*, void*, void*,
+    unsigned int*, unsigned int*, float*, int*, unsigned int*,
+    int max_seq_len, int group_size, qwen35_stream_t stream) {
+    if (group_size != 32) { q35::set_error("NVFP4 decode supports group_size 32 (got %d)", group_size); return QWEN35_ERR_UNSUPPORTED; }
+    if (!token_ids || seq_len <= 0) { q35::set_error("prefill_megakernel_nvfp4: no prompt tokens"); return QWEN35_ERR_BAD_ARG; }
+    q35::DecodeArgs a = {};
+    a.layers = layer_weights; a.embed = (const q35::bf16*)embed_weight; a.final_norm = (const q35::bf16*)final_norm_weight;
+    a.lm_head = (const q35::bf16*)lm_head_weight_packed; a.lm_scales = lm_head_scales;
+    a.k_cache = (q35::bf16*)fa_k_cache; a.v_cache = (q35::bf16*)fa_v_cache; a.dn_states = (float*)dn_states; a.conv_bufs = (float*)conv_bufs;
+    a.forced_ids = token_ids; a.out_token = output_token_id; a.hidden_out = (q35::bf16*)hidden_buffer;
+    a.position = 0; a.max_seq_len = max_seq_len; a.n_steps = seq_len; a.lm_last_only = 1;
+    return q35::launch_decode_impl(a, (cudaStream_t)stream, false, true);
 }
 
 // Extended NVFP4 decode: the arguments of qwen35_b200_decode_steps (layer table in the NVFP4 record layout,

@@ -255,10 +255,10 @@ extern "C" int qwen35_b200_draft_forward(const Qwen35DraftArgs* in) {
     const int q = D.q_len, H = D.hidden, T = ctx + q, qd = D.n_heads * DR_HD, kvd = D.n_kv_heads * DR_HD, fc_in = D.n_target_layers * H;
     const int chunks = (T + DR_CHUNK - 1) / DR_CHUNK;
     const size_t att_smem = (size_t)(DR_ROWS + 2 * DR_CHUNK) * DR_LD * 2;
-    static bool attr_done = false;
-    if (!attr_done) {
+    static PerDeviceOnce attr_done;
+    if (attr_done.pending()) {
         Q35_CUDA_OK(cudaFuncSetAttribute(dr_attn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)att_smem));
-        attr_done = true;
+        attr_done.mark();
     }
     PdlGuard pdl_guard;      // every kernel of the forward starts with pdl_wait(): launches overlap their predecessor's drain
     // 1. feature fusion, once per call: target_feat = rms_norm(fc . target_hidden_cat) * hidden_norm -> rows 0..ctx-1 of X

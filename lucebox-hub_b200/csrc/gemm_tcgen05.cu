@@ -681,11 +681,11 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
         dim3 grid(n_tiles, m_tiles);
 #define Q35_GEMM_ROW2(E)                                                                                                                        \
     case E: {                                                                                                                                   \
-        static bool attr = false;                                                                                                               \
-        if (!attr) {                                                                                                                            \
+        static PerDeviceOnce attr;                                                                                                               \
+        if (attr.pending()) {                                                                                                                            \
             Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                              (int)gemm_smem(GEMM_STAGES_SKINNY)));                                                              \
-            attr = true;                                                                                                                        \
+            attr.mark();                                                                                                                        \
         }                                                                                                                                       \
         Q35_CUDA_OK(gemm_launch(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, false>, grid, gemm_smem(GEMM_STAGES_SKINNY), stream, tmA, tmB, p));      \
         break;                                                                                                                                  \
@@ -696,11 +696,11 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
         dim3 grid(n_tiles, m_tiles);
 #define Q35_GEMM_WIDE(E)                                                                                                                      \
     case E: {                                                                                                                                 \
-        static bool attr = false;                                                                                                             \
-        if (!attr) {                                                                                                                          \
+        static PerDeviceOnce attr;                                                                                                             \
+        if (attr.pending()) {                                                                                                                          \
             Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_WIDE, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                              (int)gemm_smem(GEMM_STAGES_WIDE)));                                                              \
-            attr = true;                                                                                                                      \
+            attr.mark();                                                                                                                      \
         }                                                                                                                                     \
         Q35_CUDA_OK(gemm_launch(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_WIDE, false>, grid, gemm_smem(GEMM_STAGES_WIDE), stream, tmA, tmB, p));        \
         break;                                                                                                                                \
@@ -715,11 +715,11 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
             dim3 grid(n_tiles, m_tiles);
 #define Q35_GEMM_ROW(E)                                                                                                                         \
     case E: {                                                                                                                                   \
-        static bool attr = false;                                                                                                               \
-        if (!attr) {                                                                                                                            \
+        static PerDeviceOnce attr;                                                                                                               \
+        if (attr.pending()) {                                                                                                                            \
             Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
                                              (int)gemm_smem(GEMM_STAGES_SKINNY)));                                                              \
-            attr = true;                                                                                                                        \
+            attr.mark();                                                                                                                        \
         }                                                                                                                                       \
         Q35_CUDA_OK(gemm_launch(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, false>, grid, gemm_smem(GEMM_STAGES_SKINNY), stream, tmA, tmB, p));      \
         break;                                                                                                                                  \
@@ -743,11 +743,11 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
         cfg.attrs = at; cfg.numAttrs = g_pdl_launch ? 2 : 1;
 #define Q35_GEMM_SKINNY(E)                                                                                                                       \
     case E: {                                                                                                                                    \
-        static bool attr = false;                                                                                                                \
-        if (!attr) {                                                                                                                             \
+        static PerDeviceOnce attr;                                                                                                                \
+        if (attr.pending()) {                                                                                                                             \
             Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
                                              (int)gemm_smem(GEMM_STAGES_SKINNY)));                                                               \
-            attr = true;                                                                                                                         \
+            attr.mark();                                                                                                                         \
         }                                                                                                                                        \
         Q35_CUDA_OK(cudaLaunchKernelEx(&cfg, gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, true>, tmA, tmB, p));                                \
         break;                                                                                                                                   \
@@ -806,10 +806,10 @@ int gemm_q4k(const bf16* A, int lda, const uint8_t* W, int w_rows, bf16* C, int 
     cfg.attrs = at; cfg.numAttrs = g_pdl_launch ? 2 : 1;
 #define Q35_GEMM_Q4K(E)                                                                                                            \
     case E: {                                                                                                                      \
-        static bool attr = false;                                                                                                  \
-        if (!attr) {                                                                                                               \
+        static PerDeviceOnce attr;                                                                                                  \
+        if (attr.pending()) {                                                                                                               \
             Q35_CUDA_OK(cudaFuncSetAttribute(gemm_q4k_tcgen05_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Q4K_SMEM)); \
-            attr = true;                                                                                                           \
+            attr.mark();                                                                                                           \
         }                                                                                                                          \
         Q35_CUDA_OK(cudaLaunchKernelEx(&cfg, gemm_q4k_tcgen05_kernel<E>, tmA, tmW, qp));                                                 \
         break;                                                                                                                     \

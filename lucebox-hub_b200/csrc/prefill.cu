@@ -20,12 +20,6 @@ namespace q35 {
 int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ldc, const bf16* R, int ldr,
               int M, int N, int K, int epi, int up_row_offset, cudaStream_t stream);
 
-struct PrefillFused {            // reference: struct PrefillFusedLayerWeights (torch_bindings.cpp:31-38, prefill.cu:66-73)
-    const void* proj_weight;     // DN: [qkv; z; b; a] = 8224 x 1024, FA: [q; k; v] = 5120 x 1024
-    const void* gate_up_weight;  // [gate; up] = 7168 x 1024
-    const void* unused[4];       // NVFP4 copies of the same matrices (not read by the BF16 path)
-};
-
 // grow-only per-device scratch for the chunk-local results
 static void* g_scratch[64] = {};
 static size_t g_scratch_bytes[64] = {};
@@ -56,6 +50,8 @@ struct PrefillArgs {
     float* logits_out;
     const void* lm_packed;     // optional NVFP4 LM head (tensor-core layout) for the last token
     const void* lm_scales;
+    const bf16* dbg_teacher;   // optional [layers][S][HIDDEN]: input of layer l > 0
+    bf16* dbg_hidden;          // optional [layers][HIDDEN]: last position's output of every layer
     int max_seq_len;
     int n_layers;
 };
@@ -68,12 +64,12 @@ struct PrefillArgs {
 
 static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
     const int S = a.S;
-    static bool attr_done = false;
-    if (!attr_done) {
+    static PerDeviceOnce attr_done;
+    if (attr_done.pending()) {
         Q35_CUDA_OK(cudaFuncSetAttribute(pf_dn_chunk_local_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CHUNK_LOCAL_SMEM));
         Q35_CUDA_OK(cudaFuncSetAttribute(pf_dn_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CHUNK_SCAN_SMEM));
         Q35_CUDA_OK(cudaFuncSetAttribute(pf_attention_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_MMA_SMEM));
-        attr_done = true;
+        attr_done.mark();
     }
     const int nchunks = (S + DN_CHUNK - 1) / DN_CHUNK;
     ChunkScratch* scratch = (ChunkScratch*)get_scratch((size_t)DN_HEADS * nchunks * sizeof(ChunkScratch));
@@ -86,15 +82,25 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
     PdlGuard pdl_guard;
     for (int layer = 0; layer < a.n_layers; ++layer) {
         const LayerRec& L = a.layers_host[layer];
-        const PrefillFused& F = a.fused_host[layer];
-        // input norm (layer 0 gathers the embedding rows into `hidden` on the way)
-        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, S, 128, 0, stream, layer == 0 ? a.token_ids : nullptr, a.embed, a.hidden, (const bf16*)L.p[0],
+        // Without fused tables (launch_prefill_bf16_mega) every matrix of the layer record is its own GEMM, written into the
+        // same column blocks of proj_buf the fused projection fills, and SiLU * up is a kernel of its own.
+        const PrefillFused* F = a.fused_host ? &a.fused_host[layer] : nullptr;
+        // input norm (layer 0 gathers the embedding rows into `hidden` on the way); with a teacher, layer l > 0 takes its
+        // input (and the residual of its mixer) from the teacher's row block instead of the previous layer's output
+        const bf16* layer_in = (a.dbg_teacher && layer > 0) ? a.dbg_teacher + (size_t)layer * S * HIDDEN : a.hidden;
+        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, S, 128, 0, stream, layer == 0 ? a.token_ids : nullptr, a.embed, layer_in, (const bf16*)L.p[0],
                                                  layer == 0 ? a.hidden : nullptr, a.normalized, S));
         g_launches.fetch_add(1);
         const bf16 *w_out, *w_post, *w_down;
         if (L.type == 0) {
             const int ldp = DN_PROJ_ROWS;
-            Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)F.proj_weight, DN_PROJ_ROWS, a.proj_buf, ldp, nullptr, 0, S, DN_PROJ_ROWS, HIDDEN, 0, 0, stream));
+            if (F) {
+                Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)F->proj_weight, DN_PROJ_ROWS, a.proj_buf, ldp, nullptr, 0, S, DN_PROJ_ROWS, HIDDEN, 0, 0, stream));
+            } else {
+                const int slot[4] = {DN_QKV, DN_Z, DN_B, DN_A}, rows[4] = {DN_CONV_CH, DN_V_SIZE, DN_HEADS, DN_HEADS};
+                for (int i = 0, col = 0; i < 4; col += rows[i], ++i)
+                    Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)L.p[slot[i]], rows[i], a.proj_buf + col, ldp, nullptr, 0, S, rows[i], HIDDEN, 0, 0, stream));
+            }
             Q35_CUDA_OK(pdl_launch(pf_dn_prep_kernel, dim3(S, DN_HEADS), 128, 0, stream, a.proj_buf, ldp, (const bf16*)L.p[DN_CONV], (const bf16*)L.p[DN_ALOG],
                                                                       (const bf16*)L.p[DN_DTBIAS], a.proj_buf2, a.beta_buf, a.alpha_buf, S));
             Q35_CUDA_OK(pdl_launch(pf_conv_state_kernel, (DN_CONV_CH + 255) / 256, 256, 0, stream, a.proj_buf, ldp, a.conv_bufs + (size_t)i_dn * DN_CONV_CH * 4, S));
@@ -107,7 +113,13 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
             ++i_dn;
         } else {
             const int ldp = FA_PROJ_ROWS;
-            Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)F.proj_weight, FA_PROJ_ROWS, a.proj_buf, ldp, nullptr, 0, S, FA_PROJ_ROWS, HIDDEN, 0, 0, stream));
+            if (F) {
+                Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)F->proj_weight, FA_PROJ_ROWS, a.proj_buf, ldp, nullptr, 0, S, FA_PROJ_ROWS, HIDDEN, 0, 0, stream));
+            } else {
+                const int slot[3] = {FA_Q, FA_K, FA_V}, rows[3] = {FA_QPROJ, FA_KV_SIZE, FA_KV_SIZE};
+                for (int i = 0, col = 0; i < 3; col += rows[i], ++i)
+                    Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)L.p[slot[i]], rows[i], a.proj_buf + col, ldp, nullptr, 0, S, rows[i], HIDDEN, 0, 0, stream));
+            }
             bf16* kc = a.k_cache + (size_t)i_fa * FA_KV_HEADS * a.max_seq_len * FA_HEAD_DIM;
             bf16* vc = a.v_cache + (size_t)i_fa * FA_KV_HEADS * a.max_seq_len * FA_HEAD_DIM;
             Q35_CUDA_OK(pdl_launch(pf_qk_norm_rope_kernel, (S * 12 + 7) / 8, 256, 0, stream, a.proj_buf, ldp, (const bf16*)L.p[FA_QNORM], (const bf16*)L.p[FA_KNORM], rt,
@@ -119,11 +131,23 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
             ++i_fa;
         }
         // output projection + residual -> residual buffer holds the hidden state after the mixer
-        Q35_TRY(gemm_bf16(a.attn_buf, 2048, w_out, HIDDEN, a.residual, HIDDEN, a.hidden, HIDDEN, S, HIDDEN, 2048, 1, 0, stream));
+        Q35_TRY(gemm_bf16(a.attn_buf, 2048, w_out, HIDDEN, a.residual, HIDDEN, layer_in, HIDDEN, S, HIDDEN, 2048, 1, 0, stream));
         Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, S, 128, 0, stream, nullptr, nullptr, a.residual, w_post, nullptr, a.normalized, S));
         g_launches.fetch_add(1);
-        Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)F.gate_up_weight, 2 * INTER, a.mlp_buf, INTER, nullptr, 0, S, INTER, HIDDEN, 2, INTER, stream));
+        if (F) {
+            Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)F->gate_up_weight, 2 * INTER, a.mlp_buf, INTER, nullptr, 0, S, INTER, HIDDEN, 2, INTER, stream));
+        } else {
+            // the projection buffers are free again here: gate -> proj_buf, up -> proj_buf2 (both [S, 3584])
+            const bool dn = L.type == 0;
+            Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)L.p[dn ? (int)DN_GATE : (int)FA_GATE], INTER, a.proj_buf, INTER, nullptr, 0, S, INTER, HIDDEN, 0, 0, stream));
+            Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)L.p[dn ? (int)DN_UP : (int)FA_UP], INTER, a.proj_buf2, INTER, nullptr, 0, S, INTER, HIDDEN, 0, 0, stream));
+            const int n8 = S * INTER / 8;
+            Q35_CUDA_OK(pdl_launch(pf_silu_mul_kernel, (n8 + 255) / 256, 256, 0, stream, (const bf16*)a.proj_buf, (const bf16*)a.proj_buf2, a.mlp_buf, n8));
+            g_launches.fetch_add(1);
+        }
         Q35_TRY(gemm_bf16(a.mlp_buf, INTER, w_down, HIDDEN, a.hidden, HIDDEN, a.residual, HIDDEN, S, HIDDEN, INTER, 1, 0, stream));
+        if (a.dbg_hidden)
+            Q35_CUDA_OK(cudaMemcpyAsync(a.dbg_hidden + (size_t)layer * HIDDEN, a.hidden + (size_t)(S - 1) * HIDDEN, HIDDEN * sizeof(bf16), cudaMemcpyDeviceToDevice, stream));
     }
     // last token: final norm, LM head, arg-max
     const bf16* last = a.hidden + (size_t)(S - 1) * HIDDEN;
@@ -144,31 +168,35 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
 // they are read back once per distinct pair of table pointers and kept on the host, so later calls neither
 // synchronise nor allocate (a prefill can then be captured in a CUDA graph).  A caller that frees its tables and
 // packs new ones can get the same device address back with different contents: it calls
-// qwen35_b200_forget_tables() after re-packing (the Python host does so whenever it packs).
-struct HostTables { const void* dev_layers; const void* dev_fused; LayerRec layers[NUM_LAYERS]; PrefillFused fused[NUM_LAYERS]; };
+// qwen35_b200_forget_tables() after re-packing (both Python hosts do so whenever a table tensor they have not seen
+// appears).  The caller receives a COPY made under the lock, so an entry that is evicted or forgotten while another
+// thread is still launching from its copy cannot dangle.  dev_fused may be null (launch_prefill_bf16_mega has none).
 static HostTables g_tables[8];
-static int g_tables_n = 0;
+static int g_tables_n = 0, g_tables_next = 0;
 static std::mutex g_tables_mu;
 
-const void* host_layer_tables(const void* dev_layers, const void* dev_fused, const void** fused_out) {
+bool host_layer_tables(const void* dev_layers, const void* dev_fused, HostTables* out) {
     std::lock_guard<std::mutex> lk(g_tables_mu);
     for (int i = 0; i < g_tables_n; ++i)
-        if (g_tables[i].dev_layers == dev_layers && g_tables[i].dev_fused == dev_fused) { *fused_out = g_tables[i].fused; return g_tables[i].layers; }
-    HostTables* t = &g_tables[g_tables_n < 8 ? g_tables_n++ : 7];
-    t->dev_layers = dev_layers; t->dev_fused = dev_fused;
-    if (cudaMemcpy(t->layers, dev_layers, sizeof(t->layers), cudaMemcpyDeviceToHost) != cudaSuccess ||
-        cudaMemcpy(t->fused, dev_fused, sizeof(t->fused), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        if (g_tables[i].dev_layers == dev_layers && g_tables[i].dev_fused == dev_fused) { *out = g_tables[i]; return true; }
+    HostTables t = {};
+    t.dev_layers = dev_layers; t.dev_fused = dev_fused;
+    if (cudaMemcpy(t.layers, dev_layers, sizeof(t.layers), cudaMemcpyDeviceToHost) != cudaSuccess ||
+        (dev_fused && cudaMemcpy(t.fused, dev_fused, sizeof(t.fused), cudaMemcpyDeviceToHost) != cudaSuccess)) {
         set_error("reading the layer tables failed: %s", cudaGetErrorString(cudaGetLastError()));
-        t->dev_layers = nullptr;
-        return nullptr;
+        return false;
     }
-    *fused_out = t->fused;
-    return t->layers;
+    // a full cache evicts its entries in turn
+    const int slot = g_tables_n < 8 ? g_tables_n++ : (g_tables_next++ & 7);
+    g_tables[slot] = t;
+    *out = t;
+    return true;
 }
 
 void forget_layer_tables() {
     std::lock_guard<std::mutex> lk(g_tables_mu);
     g_tables_n = 0;
+    g_tables_next = 0;
 }
 
 }  // namespace q35
@@ -182,16 +210,15 @@ extern "C" int qwen35_b200_prefill_bf16(const Qwen35PrefillArgs* in, qwen35_stre
         set_error("seq_len %d out of range (max_seq_len %d, library limit %d)", in->seq_len, in->max_seq_len, ATT_PF_MAX_S);
         return QWEN35_ERR_BAD_ARG;
     }
-    if (!in->token_ids || !in->embed_weight || !in->layer_weights || !in->fused_layer_weights || !in->hidden || !in->proj_buf) {
+    if (!in->token_ids || !in->embed_weight || !in->layer_weights || !in->hidden || !in->proj_buf) {
         set_error("null tensor pointer");
         return QWEN35_ERR_BAD_ARG;
     }
-    const void* fused_h = nullptr;
-    const void* layers_h = host_layer_tables(in->layer_weights, in->fused_layer_weights, &fused_h);
-    if (!layers_h) return QWEN35_ERR_CUDA;
+    HostTables tables;
+    if (!host_layer_tables(in->layer_weights, in->fused_layer_weights, &tables)) return QWEN35_ERR_CUDA;
     PrefillArgs a = {};
     a.token_ids = in->token_ids; a.S = in->seq_len; a.out_token = in->out_token;
-    a.embed = (const bf16*)in->embed_weight; a.layers_host = (const LayerRec*)layers_h; a.fused_host = (const PrefillFused*)fused_h;
+    a.embed = (const bf16*)in->embed_weight; a.layers_host = tables.layers; a.fused_host = in->fused_layer_weights ? tables.fused : nullptr;
     a.final_norm = (const bf16*)in->final_norm_weight; a.lm_head = (const bf16*)in->lm_head_weight;
     a.k_cache = (bf16*)in->fa_k_cache; a.v_cache = (bf16*)in->fa_v_cache; a.dn_states = (float*)in->dn_states; a.conv_bufs = (float*)in->conv_bufs;
     a.hidden = (bf16*)in->hidden; a.residual = (bf16*)in->residual; a.normalized = (bf16*)in->normalized;
@@ -201,6 +228,7 @@ extern "C" int qwen35_b200_prefill_bf16(const Qwen35PrefillArgs* in, qwen35_stre
     a.lm_bmv = (float*)in->lm_bmv; a.lm_bmi = (int*)in->lm_bmi; a.logits_out = in->logits_out;
     a.lm_packed = in->lm_head_weight_packed; a.lm_scales = in->lm_head_scales;
     a.max_seq_len = in->max_seq_len;
+    a.dbg_teacher = (const bf16*)in->dbg_teacher; a.dbg_hidden = (bf16*)in->dbg_hidden;
     a.n_layers = in->dbg_num_layers > 0 ? in->dbg_num_layers : NUM_LAYERS;
     return prefill_impl(a, (cudaStream_t)stream);
 }
@@ -248,5 +276,30 @@ extern "C" int launch_prefill_bf16_nvfp4_lm(
     a.attn_buf = attn_buf; a.mlp_buf = mlp_buf; a.dn_out_buf = dn_out_buf; a.beta_buf = beta_buf; a.alpha_buf = alpha_buf;
     a.final_normed = final_normed; a.hidden_bf16_out = hidden_bf16_out; a.lm_bmv = lm_bmv; a.lm_bmi = lm_bmi;
     a.max_seq_len = 2048;
+    return qwen35_b200_prefill_bf16(&a, stream);
+}
+
+// Replaces launch_prefill_bf16_mega (torch_bindings.cpp:354-364; prefill_megakernel.cu:840-1078), the reference's
+// single-dispatch prompt pass.  Same results as launch_prefill_bf16; it has no fused-weight table, so each matrix of the
+// layer records runs as its own tensor-core GEMM (the reference's version does the same work from one persistent grid at
+// 58.6 ms for 520 tokens; this one is a stream of launches chained by programmatic dependent launch).
+extern "C" int launch_prefill_bf16_mega(
+    const int* token_ids, int seq_len, int* output_token,
+    const void* embed_weight, const LayerWeights* layers,
+    const void* final_norm_w, const void* lm_head_w,
+    void* fa_k_cache, void* fa_v_cache, void* dn_states, void* conv_bufs,
+    void* hidden, void* residual, void* normalized,
+    void* proj_buf, void* proj_buf2, void* attn_buf, void* mlp_buf,
+    void* dn_out_buf, void* beta_buf, void* alpha_buf,
+    void* final_normed, void* hidden_bf16_out, void* lm_bmv, void* lm_bmi, qwen35_stream_t stream) {
+    Qwen35PrefillArgs a = {};
+    a.token_ids = token_ids; a.seq_len = seq_len; a.out_token = output_token;
+    a.embed_weight = embed_weight; a.layer_weights = layers; a.fused_layer_weights = nullptr;
+    a.final_norm_weight = final_norm_w; a.lm_head_weight = lm_head_w;
+    a.fa_k_cache = fa_k_cache; a.fa_v_cache = fa_v_cache; a.dn_states = dn_states; a.conv_bufs = conv_bufs;
+    a.hidden = hidden; a.residual = residual; a.normalized = normalized; a.proj_buf = proj_buf; a.proj_buf2 = proj_buf2;
+    a.attn_buf = attn_buf; a.mlp_buf = mlp_buf; a.dn_out_buf = dn_out_buf; a.beta_buf = beta_buf; a.alpha_buf = alpha_buf;
+    a.final_normed = final_normed; a.hidden_bf16_out = hidden_bf16_out; a.lm_bmv = lm_bmv; a.lm_bmi = lm_bmi;
+    a.max_seq_len = 2048;       // MAX_SEQ of the reference's megakernel (prefill_megakernel.cu:37)
     return qwen35_b200_prefill_bf16(&a, stream);
 }

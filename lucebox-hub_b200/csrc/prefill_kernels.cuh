@@ -53,6 +53,23 @@ static __global__ void __launch_bounds__(128) pf_rmsnorm_kernel(const int* __res
     *(reinterpret_cast<uint4*>(x_out + (size_t)t * HIDDEN) + tid) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// ---- silu(gate) * up over [S, INTER] bf16 buffers, 8 values per thread: the epilogue of the fused [gate; up] GEMM as a
+// kernel of its own, for callers whose tables hold gate and up as two matrices.  Same roundings: bf16(silu(g)) * u -> bf16.
+static __global__ void __launch_bounds__(256) pf_silu_mul_kernel(const bf16* __restrict__ gate, const bf16* __restrict__ up, bf16* __restrict__ out, int n8) {
+    pdl_wait();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n8) return;
+    const uint4 g = reinterpret_cast<const uint4*>(gate)[i], u = reinterpret_cast<const uint4*>(up)[i];
+    const uint32_t gw[4] = {g.x, g.y, g.z, g.w}, uw[4] = {u.x, u.y, u.z, u.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const __nv_bfloat162 pr = __halves2bfloat162(f2bf(rbf(silu_f(bf_lo(gw[j]))) * bf_lo(uw[j])), f2bf(rbf(silu_f(bf_hi(gw[j]))) * bf_hi(uw[j])));
+        o[j] = *reinterpret_cast<const uint32_t*>(&pr);
+    }
+    reinterpret_cast<uint4*>(out)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 // ---- DeltaNet preparation: one CTA (128 threads) per (token, head) -----------------------------------
 // proj: [S, ldp] bf16 rows [qkv 6144 | z 2048 | b 16 | a 16].  Writes qkv_out [S, 6144] bf16 (q, k L2-normalised
 // in bf16 arithmetic, v after conv + SiLU), beta [S,16] (bf16-rounded sigmoid), g [S,16] (f32 log-decay).

@@ -11,6 +11,7 @@ namespace q35 {
 static constexpr int MAX_DEVICES = 64;
 static void* g_ws[MAX_DEVICES] = {};
 static int g_sms[MAX_DEVICES] = {};
+static int* g_extra_status[MAX_DEVICES] = {};
 static std::mutex g_mu;
 static thread_local char g_err[512] = "";
 std::atomic<long long> g_launches{0};
@@ -43,8 +44,6 @@ void* get_workspace() {
     return g_ws[dev];
 }
 
-static int* g_extra_status[MAX_DEVICES] = {};
-
 void register_status_word(int* dev_ptr) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) return;
@@ -61,31 +60,44 @@ int device_sm_count() {
 
 }  // namespace q35
 
+// Status words that exist on the current device: the regular workspace's (only if some earlier call already
+// allocated it) and the one registered for the static scratch.  Reading the status never creates either.
+static int existing_status_words(int* out[2]) {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= q35::MAX_DEVICES) return 0;
+    std::lock_guard<std::mutex> lk(q35::g_mu);
+    if (q35::g_ws[dev]) out[n++] = (int*)q35::g_ws[dev];
+    if (q35::g_extra_status[dev]) out[n++] = q35::g_extra_status[dev];
+    return n;
+}
+
 extern "C" int qwen35_b200_status(qwen35_stream_t stream) {
     using namespace q35;
-    void* ws = get_workspace();
-    if (!ws) return QWEN35_ERR_CUDA;
-    int err = 0;
-    Q35_CUDA_OK(cudaMemcpyAsync(&err, ws, sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream));
-    int dev = 0;
-    int err2 = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < MAX_DEVICES && g_extra_status[dev])
-        Q35_CUDA_OK(cudaMemcpyAsync(&err2, g_extra_status[dev], sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream));
+    int* words[2];
+    const int n = existing_status_words(words);
+    int err[2] = {0, 0};
+    for (int i = 0; i < n; ++i)
+        Q35_CUDA_OK(cudaMemcpyAsync(&err[i], words[i], sizeof(int), cudaMemcpyDeviceToHost, (cudaStream_t)stream));
     Q35_CUDA_OK(cudaStreamSynchronize((cudaStream_t)stream));
-    if (!err) err = err2;
-    if (err) set_error("device status %d (%s)", err, err == 1 ? "a bounded device-side wait ran out" : "bad argument seen on device");
-    return err;
+    const int e = err[0] ? err[0] : err[1];
+    if (e) set_error("device status %d (%s)", e, e == 1 ? "a bounded device-side wait ran out" : "bad argument seen on device");
+    return e;
 }
 
 extern "C" int qwen35_b200_clear_status(qwen35_stream_t stream) {
     using namespace q35;
-    void* ws = get_workspace();
-    if (!ws) return QWEN35_ERR_CUDA;
-    Q35_CUDA_OK(cudaMemsetAsync(ws, 0, 256, (cudaStream_t)stream));
-    int dev = 0;
-    if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < MAX_DEVICES && g_extra_status[dev])
-        Q35_CUDA_OK(cudaMemsetAsync(g_extra_status[dev], 0, sizeof(int), (cudaStream_t)stream));
+    int* words[2];
+    const int n = existing_status_words(words);
+    for (int i = 0; i < n; ++i) Q35_CUDA_OK(cudaMemsetAsync(words[i], 0, sizeof(int), (cudaStream_t)stream));
     return QWEN35_OK;
+}
+
+/* Address of the library-allocated workspace of the current device, or NULL while no call has created it (tests). */
+extern "C" const void* qwen35_b200_workspace_if_any(void) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= q35::MAX_DEVICES) return nullptr;
+    std::lock_guard<std::mutex> lk(q35::g_mu);
+    return q35::g_ws[dev];
 }
 
 extern "C" long long qwen35_b200_launch_count(void) { return q35::g_launches.load(); }

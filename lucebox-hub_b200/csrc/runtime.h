@@ -24,6 +24,15 @@ extern std::atomic<long long> g_launches;
 // serialization attribute to their launches (the GEMM kernels call pdl_wait() after their prologue)
 extern bool g_pdl_launch;
 
+// cudaFuncSetAttribute acts on the current device only, so a launcher's "attribute set" flag is kept per device.
+// Two host threads that race here both set the attribute, which is harmless.
+struct PerDeviceOnce {
+    std::atomic<bool> done[64] = {};
+    static int slot() { int d = 0; return cudaGetDevice(&d) == cudaSuccess ? (d & 63) : 0; }
+    bool pending() const { return !done[slot()].load(std::memory_order_acquire); }
+    void mark() { done[slot()].store(true, std::memory_order_release); }
+};
+
 #define Q35_CUDA_OK(expr)                                                         \
     do {                                                                          \
         cudaError_t e__ = (expr);                                                 \

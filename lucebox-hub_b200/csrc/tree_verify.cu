@@ -839,18 +839,20 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
     const int R = n * gqa, mt_n = (R + 15) / 16;
     const size_t sc_smem = ((size_t)mt_n * 16 * TV_QSTRIDE + (size_t)TV_CHUNK * TV_QSTRIDE) * 2;
     const size_t pv_smem = ((size_t)TV_CHUNK * TV_QSTRIDE + (size_t)mt_n * 16 * TV_PSTRIDE) * 2;
-    static bool attr_done = false;
-    if (!attr_done) {
+    static PerDeviceOnce attr_done;
+    if (attr_done.pending()) {
         Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_scores_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
         Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_scores_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
         Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_pv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
         Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_pv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
         Q35_CUDA_OK(cudaFuncSetAttribute(tv_dn_tree_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tv_dn_tree_smem(TV_MAX_NODES)));
-        attr_done = true;
+        attr_done.mark();
     }
     // second stream for the work that runs beside a projection; made once for the process's device and forked from /
     // joined into the caller's stream with events, so it is also legal inside a stream capture
-    static struct { cudaStream_t stream = nullptr; cudaEvent_t fork = nullptr, join = nullptr; } side;
+    struct SideStream { cudaStream_t stream = nullptr; cudaEvent_t fork = nullptr, join = nullptr; };
+    static SideStream side_of[64];                       // streams and events belong to a device: one set per device
+    SideStream& side = side_of[PerDeviceOnce::slot()];
     if (!side.stream) {
         Q35_CUDA_OK(cudaStreamCreateWithFlags(&side.stream, cudaStreamNonBlocking));
         Q35_CUDA_OK(cudaEventCreateWithFlags(&side.fork, cudaEventDisableTiming));

@@ -43,6 +43,7 @@ class PrefillArgs(C.Structure):
         ("final_normed", C.c_void_p), ("hidden_bf16_out", C.c_void_p), ("lm_bmv", C.c_void_p), ("lm_bmi", C.c_void_p),
         ("logits_out", C.c_void_p), ("max_seq_len", C.c_int), ("dbg_num_layers", C.c_int),
         ("lm_head_weight_packed", C.c_void_p), ("lm_head_scales", C.c_void_p),
+        ("dbg_teacher", C.c_void_p), ("dbg_hidden", C.c_void_p),
     ]
 
 
@@ -113,6 +114,8 @@ SIGNATURES = {
     "qwen35_b200_prefill_bf16": (_i, [C.POINTER(PrefillArgs), _vp]),
     "launch_prefill_bf16_nvfp4_lm": (_i, [_vp, _i, _vp] + [_vp] * 7 + [_vp] * 4 + [_vp] * 3 + [_vp] * 5 + [_vp] * 5 + [_vp] * 4 + [_vp] * 4 + [_vp]),
     "launch_prefill_bf16": (_i, [_vp, _i, _vp] + [_vp] * 5 + [_vp] * 4 + [_vp] * 3 + [_vp] * 5 + [_vp] * 5 + [_vp] * 4 + [_vp]),
+    "launch_prefill_bf16_mega": (_i, [_vp, _i, _vp] + [_vp] * 4 + [_vp] * 4 + [_vp] * 3 + [_vp] * 4 + [_vp] * 3 + [_vp] * 4 + [_vp]),
+    "launch_prefill_megakernel_nvfp4": (_i, [_vp, _i, _vp] + [_vp] * 5 + [_vp] * 4 + [_vp] * 5 + [_vp] * 10 + [_vp] * 5 + [_i, _i, _vp]),
     "launch_quantize_nvfp4_out": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp]),
     "launch_quantize_nvfp4_lm_out": (_i, [_vp, _i, _i, _vp, _vp, _vp]),
     "qwen35_b200_decode_batched": (_i, [C.POINTER(BatchedArgs), _vp]),
@@ -131,6 +134,7 @@ SIGNATURES = {
     "qwen35_b200_gemm_q4k": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "qwen35_b200_status": (_i, [_vp]),
     "qwen35_b200_clear_status": (_i, [_vp]),
+    "qwen35_b200_workspace_if_any": (_vp, []),
     "qwen35_b200_debug_read": (_i, [_i, _vp]),
     "qwen35_b200_rope_inv_freq": (_i, [C.POINTER(C.c_float)]),
     "qwen35_b200_launch_count": (C.c_longlong, []),

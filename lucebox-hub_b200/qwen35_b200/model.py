@@ -195,6 +195,8 @@ def _pack_prefill_fused_layer_weights(fused_layer_data, device="cuda"):
 
 def _pack_layer_weights(layer_data, device="cuda"):
     """Device blob of 24 records {int type; int pad[3]; void* ptrs[14]} (model.py:410-427)."""
+    if str(device) != "cpu":
+        _capi.lib().qwen35_b200_forget_tables()   # a new table may reuse the address of a freed one
     ptr_size, max_ptrs, header = 8, 14, 16
     rec = header + max_ptrs * ptr_size
     buf = bytearray(len(layer_data) * rec)
@@ -349,11 +351,13 @@ class Decoder:
         self._prefill_buffer_tokens = max_tokens
         return self._prefill_buffers
 
-    def prefill_tokens(self, token_ids: torch.Tensor, logits_out=None, mode="batched", dbg_num_layers=0) -> int:
+    def prefill_tokens(self, token_ids: torch.Tensor, logits_out=None, mode="batched", dbg_num_layers=0,
+                       dbg_teacher=None, dbg_hidden=None) -> int:
         """Reset, run the prompt, return the first generated token (reference model.py:745-799).
         mode="batched": tensor-core GEMMs + chunk-64 gated delta rule + causal attention (the
         reference's prefill_bf16 op).  mode="serial": the decode megakernel token by token (the
-        reference's token-serial `prefill_megakernel`, kernel_gb10_nvfp4.cu:1659-1755)."""
+        reference's token-serial `prefill_megakernel`, kernel_gb10_nvfp4.cu:1659-1755).  mode="mega": the
+        batched pass without the fused-weight table, one GEMM per matrix (the reference's prefill_bf16_mega op)."""
         if token_ids.device.type != "cuda" or token_ids.dtype != torch.int32 or token_ids.dim() != 1:
             raise TypeError("token_ids must be a 1D CUDA int32 tensor")
         self.reset()
@@ -368,7 +372,7 @@ class Decoder:
             a = _capi.PrefillArgs()
             a.token_ids = token_ids.data_ptr(); a.seq_len = n; a.out_token = self._out_token.data_ptr()
             a.embed_weight = self._embed_weight.data_ptr(); a.layer_weights = self._layer_weights_packed.data_ptr()
-            a.fused_layer_weights = self._prefill_fused_weights_packed.data_ptr()
+            a.fused_layer_weights = None if mode == "mega" else self._prefill_fused_weights_packed.data_ptr()
             a.final_norm_weight = self._final_norm_weight.data_ptr(); a.lm_head_weight = self._lm_head_weight.data_ptr()
             a.fa_k_cache = self._fa_k_cache.data_ptr(); a.fa_v_cache = self._fa_v_cache.data_ptr()
             a.dn_states = self._dn_states.data_ptr(); a.conv_bufs = self._conv_bufs.data_ptr()
@@ -376,6 +380,7 @@ class Decoder:
                       "beta_buf", "alpha_buf", "final_normed", "hidden_bf16_out", "lm_bmv", "lm_bmi"):
                 setattr(a, k, b[k].data_ptr())
             a.logits_out = _capi.ptr(logits_out); a.max_seq_len = self.max_seq_len; a.dbg_num_layers = dbg_num_layers
+            a.dbg_teacher = _capi.ptr(dbg_teacher); a.dbg_hidden = _capi.ptr(dbg_hidden)
             with torch.cuda.device(self.device):
                 _capi.check(self._lib.qwen35_b200_prefill_bf16(C.byref(a), self._stream()), "prefill_bf16")
             self._hidden.copy_(b["hidden_bf16_out"])
@@ -470,6 +475,10 @@ class BatchedDecoder:
         self.tokens = torch.zeros(self.batch, dtype=torch.int32, device=dev)
         self._out = torch.zeros(self.batch, dtype=torch.int32, device=dev)
         self._one = None
+        # Positions advance on the device; the host keeps an upper bound on the largest one (every step adds one) so that a
+        # step or a graph replay that would write past max_ctx is refused here.  A caller that writes `positions` directly
+        # is still covered by the kernels' own check, which skips the sequence and sets the status word.
+        self._max_position = 0
         self._streams, self._group_scratch = [], []
         if self.groups > 1:
             nb = self._lib.qwen35_b200_batched_scratch_bytes(self.batch // self.groups, self.max_ctx)
@@ -493,6 +502,7 @@ class BatchedDecoder:
         self.conv_bufs[seq].copy_(conv_bufs)
         self.positions[seq] = L
         self.tokens[seq] = int(next_token)
+        self._max_position = max(self._max_position, L)
 
     def prefill(self, seq, token_ids):
         """Prefill one sequence with the bs=1 prefill path and install it."""
@@ -553,6 +563,10 @@ class BatchedDecoder:
         """One greedy token for every sequence; the new tokens become the next step's inputs.  Returns int32 [batch]
         (GPU; the same buffer every step: clone it to keep a value).  graph=True replays a CUDA graph of the step's
         launches (recorded on the second such call: the first runs eagerly so the library's scratch exists)."""
+        if self._max_position + 1 > self.max_ctx:
+            raise ValueError(f"batched decode: a sequence is at position {self._max_position}, the cache holds max_ctx = {self.max_ctx} tokens")
+        if kw.get("advance_positions", 1):
+            self._max_position += 1
         if graph and not kw:
             if self._graph is None and self._warm:
                 g = torch.cuda.CUDAGraph()

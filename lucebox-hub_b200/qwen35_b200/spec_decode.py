@@ -28,7 +28,14 @@ class SpecDecoder:
             raise ValueError(f"budget must be 1..{MAX_NODES - 1} nodes beside the root")
         self.target, self.tw, self.D = target, target_weights, draft_dims
         self.mask_token_id, self.budget, self.temperature, self.chain_seed = int(mask_token_id), int(budget), float(temperature), bool(chain_seed)
-        self.draft_ctx_max = min(int(draft_ctx_max), target.feat_cap)
+        # A verify writes the rows of ALL its nodes (root + budget) into the ring at (past + t) % cap before the commit keeps
+        # the accepted ones.  Once past >= cap those writes land on the oldest positions still in the ring: rows
+        # [past - cap, past + budget + 1 - cap).  With at least the root accepted, the next round's window of W positions ends at
+        # past + n_acc >= past + 1, so it stays clear of the overwritten rows only while W <= cap - budget.  (The reference
+        # has cap 4096 and a window of 2048.)
+        self.draft_ctx_max = min(int(draft_ctx_max), target.feat_cap - self.budget)
+        if self.draft_ctx_max < 1:
+            raise ValueError(f"feature ring of {target.feat_cap} positions is too small for a tree budget of {self.budget}")
         head = target_weights["output_w"]
         self.draft = DraftModel(draft_dims, draft_weights, max_ctx=self.draft_ctx_max, device=target.device, lm_head=head,
                                 lm_head_q4k=head.dtype == torch.uint8, vocab=T.vocab)

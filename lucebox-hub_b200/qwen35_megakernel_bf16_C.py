@@ -6,8 +6,8 @@ quantize_nvfp4_lm_out}` with the schemas of the reference's TORCH_LIBRARY block
 (models/qwen35_0p8b/torch_bindings.cpp:529-627), for the CUDA dispatch key only.  Each op unwraps
 `data_ptr()`, takes the current CUDA stream and calls the function of libqwen35_b200.so that replaces the
 reference launcher; a non-zero status raises.  The reference's unmodified `model.py` can therefore run on top
-of this module.  Differences are listed in INTEGRATION.md (`max_seq_len` is honoured, scratch tensors are
-ignored, the prefill ops read the cache length from `fa_k_cache.size(2)`).
+of this module.  Differences: `max_seq_len` is honoured, scratch tensors are ignored, the prefill ops read
+the cache length from `fa_k_cache.size(2)`.
 """
 import ctypes as C
 
@@ -115,12 +115,36 @@ def _decode_many_nvfp4(output_tokens, token_buffer, input_token_id, embed_weight
         _capi.check(_capi.lib().qwen35_b200_decode_steps_nvfp4(C.byref(a), lm_head_scales.data_ptr(), _stream(output_tokens)), "decode_many_nvfp4")
 
 
+# The library keeps host copies of the device pointer tables, keyed by their addresses.  The reference's model.py packs
+# its tables through torch's caching allocator, which readily hands the address of a freed table to the next one, so the
+# address alone does not identify a table.  Every table TENSOR seen here is remembered by id with a weak reference; a
+# tensor that was not seen before (a re-packed table, a rebuilt Decoder) makes the library drop its copies first.
+_seen_tables = {}
+
+
+def _note_table(t):
+    if t is None:
+        return
+    key = id(t)
+    ref = _seen_tables.get(key)
+    if ref is not None and ref() is t:
+        return
+    for k in [k for k, r in _seen_tables.items() if r() is None]:
+        del _seen_tables[k]
+    import weakref
+    _seen_tables[key] = weakref.ref(t)
+    _capi.lib().qwen35_b200_forget_tables()
+
+
 def _prefill_args(output_token, token_ids, embed_weight, layer_weights_packed, fused, final_norm_weight, lm_head_weight,
                   fa_k_cache, fa_v_cache, dn_states, conv_bufs, hidden, residual, normalized, proj_buf, proj_buf2, attn_buf,
                   mlp_buf, dn_out_buf, beta_buf, alpha_buf, final_normed, hidden_bf16_out, lm_bmv, lm_bmi):
+    _note_table(layer_weights_packed)
+    _note_table(fused)
     a = _capi.PrefillArgs()
     a.token_ids = token_ids.data_ptr(); a.seq_len = int(token_ids.size(0)); a.out_token = output_token.data_ptr()
-    a.embed_weight = embed_weight.data_ptr(); a.layer_weights = layer_weights_packed.data_ptr(); a.fused_layer_weights = fused.data_ptr()
+    a.embed_weight = embed_weight.data_ptr(); a.layer_weights = layer_weights_packed.data_ptr()
+    a.fused_layer_weights = None if fused is None else fused.data_ptr()
     a.final_norm_weight = final_norm_weight.data_ptr(); a.lm_head_weight = lm_head_weight.data_ptr()
     a.fa_k_cache = fa_k_cache.data_ptr(); a.fa_v_cache = fa_v_cache.data_ptr(); a.dn_states = dn_states.data_ptr(); a.conv_bufs = conv_bufs.data_ptr()
     a.hidden = hidden.data_ptr(); a.residual = residual.data_ptr(); a.normalized = normalized.data_ptr()
@@ -173,13 +197,13 @@ def _prefill_megakernel_nvfp4(output_token, token_ids, embed_weight, layer_weigh
 def _prefill_bf16_mega(output_token, token_ids, embed_weight, layer_weights_packed, final_norm_weight, lm_head_weight, fa_k_cache,
                        fa_v_cache, dn_states, conv_bufs, hidden, residual, normalized, proj_buf, proj_buf2, attn_buf, mlp_buf,
                        dn_out_buf, beta_buf, alpha_buf, final_normed, hidden_bf16_out, lm_bmv, lm_bmi):
-    """Single-dispatch bf16 prompt pass (reference: prefill_megakernel, prefill_megakernel.cu:840-1078): the decode megakernel
-    run over the prompt, LM head after the last token."""
-    a = _steps_args(embed_weight, layer_weights_packed, final_norm_weight, lm_head_weight, fa_k_cache, fa_v_cache, dn_states,
-                    conv_bufs, hidden_bf16_out, output_token, 0, int(fa_k_cache.size(2)),
-                    forced_ids=token_ids.data_ptr(), n_steps=int(token_ids.size(0)), lm_last_only=1)
+    """The reference's single-dispatch bf16 prompt pass (prefill_megakernel, prefill_megakernel.cu:840-1078).  It takes no
+    fused-weight table, so the batched prefill runs with one tensor-core GEMM per matrix of the layer records."""
+    a = _prefill_args(output_token, token_ids, embed_weight, layer_weights_packed, None, final_norm_weight,
+                      lm_head_weight, fa_k_cache, fa_v_cache, dn_states, conv_bufs, hidden, residual, normalized, proj_buf, proj_buf2,
+                      attn_buf, mlp_buf, dn_out_buf, beta_buf, alpha_buf, final_normed, hidden_bf16_out, lm_bmv, lm_bmi)
     with torch.cuda.device(output_token.device):
-        _capi.check(_capi.lib().qwen35_b200_decode_steps(C.byref(a), _stream(output_token)), "prefill_bf16_mega")
+        _capi.check(_capi.lib().qwen35_b200_prefill_bf16(C.byref(a), _stream(output_token)), "prefill_bf16_mega")
 
 
 def _quantize_nvfp4_out(packed_out, scales_out, weight, group_size):

@@ -34,10 +34,30 @@ import torch
 import torch.nn.functional as F
 
 
+EXACT_LINEAR = False      # True: every projection is evaluated exactly (f64 sums) and rounded ONCE to the activation dtype
+
+
+def f64_to_bf16_once(x: torch.Tensor) -> torch.Tensor:
+    """float64 -> bfloat16 with a single round-to-nearest-even: first to f32 with round-to-odd (truncate toward zero, set
+    the last bit when anything was lost), after which the second rounding to 8 bits cannot double-round."""
+    y = x.to(torch.float32)
+    y64 = y.double()
+    over = y64.abs() > x.abs()
+    y = torch.where(over, torch.nextafter(y, torch.zeros_like(y)), y)
+    inexact = y.double() != x
+    bits = y.view(torch.int32)
+    bits = torch.where(inexact, bits | 1, bits)
+    return bits.view(torch.float32).to(torch.bfloat16)
+
+
 def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """Projection with f32 accumulation and one rounding to the activation dtype.  bf16 weights go through
     F.linear (what a bf16 HuggingFace model does).  f32 weights are used for the NVFP4 variant, whose dequantised
-    values (E2M1 code x fp16 or E4M3 scale) are exact in f32 but not in bf16 (kernel_gb10_nvfp4.cu:521-545)."""
+    values (E2M1 code x fp16 or E4M3 scale) are exact in f32 but not in bf16 (kernel_gb10_nvfp4.cu:521-545).
+    With EXACT_LINEAR the sum is taken in f64 (products of bf16 values are exact there and a 3584-term sum loses
+    nothing that matters at 2^-53) and rounded once: the value every f32 summation order approximates."""
+    if EXACT_LINEAR and x.dtype == torch.bfloat16:
+        return f64_to_bf16_once(F.linear(x.double(), w.double()))
     if w.dtype == x.dtype:
         return F.linear(x, w)
     return F.linear(x.float(), w.float()).to(x.dtype)
@@ -173,6 +193,7 @@ class Oracle:
         self.d = dims
         self.max_seq_len = max_seq_len
         self.state_dtype = state_dtype
+        self.keep_all = False        # True: _forward also records every position's hidden state per layer (teacher forcing of prefill)
         self.reset()
 
     def reset(self):
@@ -184,6 +205,7 @@ class Oracle:
         self.v_cache = [None] * d.n_fa
         self.last_hidden = None      # [S, hidden] bf16, output of the last layer (pre final norm)
         self.trace = []              # per layer: output hidden of the last position of the last call
+        self.trace_all = []          # per layer: output hidden of every position of the last call (only if keep_all)
 
     # ---- layer bodies -------------------------------------------------------------------
     def _deltanet(self, i_dn: int, p: list, x: torch.Tensor, use_state: bool) -> torch.Tensor:
@@ -255,7 +277,9 @@ class Oracle:
         o = o * torch.sigmoid(gate)
         return linear(o, p[6])
 
-    def _forward(self, ids: torch.Tensor, use_state: bool) -> torch.Tensor:
+    def _forward(self, ids: torch.Tensor, use_state: bool, teacher=None) -> torch.Tensor:
+        """teacher: optional per-layer list of [S, hidden] inputs; layer l > 0 then reads teacher[l] instead of the
+        previous layer's output (the layer-level comparison the GPU tests make)."""
         d = self.d
         S = ids.numel()
         if self.position + S > self.max_seq_len:
@@ -265,8 +289,11 @@ class Oracle:
         cos, sin = rope_tables(pos, d.fa_rotary_dim, d.rope_theta, h.dtype)
         i_dn = i_fa = 0
         self.trace = []
-        for ld in self.w["layer_data"]:
+        self.trace_all = []
+        for li, ld in enumerate(self.w["layer_data"]):
             p = ld["ptrs"]
+            if teacher is not None and li > 0:
+                h = teacher[li].reshape(S, -1)
             x = rmsnorm(h, p[0], d.rms_eps)
             if ld["type"] == 1:
                 y = self._attention(i_fa, p, x, cos, sin)
@@ -280,6 +307,8 @@ class Oracle:
             x = rmsnorm(h, post, d.rms_eps)
             h = h + linear(F.silu(linear(x, gate_w)) * linear(x, up_w), down_w)
             self.trace.append(h[-1])
+            if self.keep_all:
+                self.trace_all.append(h)
         self.position += S
         self.last_hidden = h
         return h
@@ -299,10 +328,10 @@ class Oracle:
         return self.logits_from_hidden(h if all_logits else h[-1])
 
     @torch.no_grad()
-    def step(self, token: int) -> torch.Tensor:
+    def step(self, token: int, teacher=None) -> torch.Tensor:
         """One cached decode step (recurrent DeltaNet form).  Returns bf16 logits [V]."""
         use_state = self.position > 0
-        h = self._forward(torch.tensor([int(token)]), use_state=use_state)
+        h = self._forward(torch.tensor([int(token)]), use_state=use_state, teacher=teacher)
         return self.logits_from_hidden(h[-1])
 
     @torch.no_grad()

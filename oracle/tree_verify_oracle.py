@@ -131,8 +131,18 @@ class TreeOracle:
         D = dims
 
         def mat(blocks):
+            # numpy releases the interpreter lock inside its array operations, so slices of a large matrix convert in parallel
             r, nb, _ = blocks.shape
-            return torch.from_numpy(q4k_gemm_operand(blocks.numpy().reshape(-1, 144))).reshape(r, nb * 256)
+            flat = blocks.numpy().reshape(-1, 144)
+            if flat.shape[0] < (1 << 16):
+                return torch.from_numpy(q4k_gemm_operand(flat)).reshape(r, nb * 256)
+            import os
+            from concurrent.futures import ThreadPoolExecutor
+            nthr = max(1, min(16, os.cpu_count() or 1))
+            parts = np.array_split(np.arange(flat.shape[0]), nthr * 4)
+            with ThreadPoolExecutor(nthr) as ex:
+                outs = list(ex.map(lambda ix: q4k_gemm_operand(flat[ix[0]:ix[-1] + 1]), [p for p in parts if len(p)]))
+            return torch.from_numpy(np.concatenate(outs, 0)).reshape(r, nb * 256)
 
         self.layers = []
         for L in weights["layers"]:

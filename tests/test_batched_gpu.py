@@ -6,8 +6,9 @@ import torch
 pytestmark = pytest.mark.gpu
 
 LAYER_ABS_TOL = 2.0 ** -5
+FRAC_TOL = 0.05                  # share of a teacher-forced trace's elements that may sit one bf16 step from the oracle's
 STATE_REL_TOL = 1e-3
-LOGIT_NOISE = 0.30
+LOGIT_TOL = 2e-2                 # teacher-forced logits: the task's bound
 
 
 def test_batched_step_matches_oracle_per_sequence(full_weights_cpu):
@@ -45,8 +46,8 @@ def test_batched_step_matches_oracle_per_sequence(full_weights_cpu):
         print(f"seq {b} (context {L}): {exact}/24 layers bit-identical, {frac:.3%} elements differ, max abs {max_abs}, max |dlogit| {float(ld.max()):.4f}")
         # projections run on tensor cores here: their f32 accumulation flips ~6e-4 of the bf16 roundings against the CPU
         # (the FMA GEMV of the bs=1 kernel: ~1e-4), so fewer layers are bit-identical; every element stays within 2^-5
-        assert exact >= 2 and frac < 0.20 and max_abs <= LAYER_ABS_TOL
-        assert float(ld.max()) <= LOGIT_NOISE
+        assert exact >= 2 and frac < FRAC_TOL and max_abs <= LAYER_ABS_TOL
+        assert float(ld.max()) <= LOGIT_TOL
         top = torch.topk(ref_logits[b], 2).values
         if float(top[0] - top[1]) > 2 * float(ld.max()):
             assert int(toks[b]) == nxt[b]
@@ -113,3 +114,88 @@ def test_batched_two_concurrent_groups_equal_one_batch(full_weights_cpu):
         runs.append((outs.cpu(), bd.positions.cpu(), bd.dn_states.cpu(), bd.conv_bufs.cpu()))
     for a, b in zip(runs[0], runs[1]):
         assert torch.equal(a, b)
+
+
+def test_batched_64_sequences_with_long_contexts(full_weights_cpu):
+    """The benchmarked batch: 64 sequences in one step, two of them at contexts beyond 2048 tokens (17 attention chunks of
+    128 positions, 33 KV pages), compared with the bs=1 oracle like the short ones; the other sequences hold short
+    contexts and are checked for running in range."""
+    from oracle.qwen35_oracle import Oracle
+    from qwen35_b200.config import QWEN35_0P8B as D
+    from qwen35_b200.model import BatchedDecoder
+    from qwen35_b200.weights import make_token_ids, weights_to
+    wg = weights_to(full_weights_cpu, "cuda")
+    B = 64
+    lens = {0: 2049, 63: 2100, 17: 5, 40: 129}
+    bd = BatchedDecoder(wg, batch=B, max_ctx=2304)
+    teacher = torch.zeros(24, B, 1024, dtype=torch.bfloat16)
+    refs = {}
+    for b in range(B):
+        L = lens.get(b, 1 + b % 7)
+        ids = make_token_ids(L + 1, 500 + b, D.vocab)
+        o = Oracle(full_weights_cpu, D, 2304)
+        o.prefill(ids[:L])
+        bd.load_sequence(b, torch.stack(o.k_cache).cuda(), torch.stack(o.v_cache).cuda(), o.dn_states_ref_layout().cuda(),
+                         o.conv_ref_layout().cuda(), L, int(ids[L]))
+        if b in lens:
+            lg = o.step(int(ids[L]))
+            tr = torch.stack(o.trace)
+            teacher[1:, b] = tr[:-1]
+            refs[b] = (o, tr, lg.float(), L)
+    dbg = torch.zeros(24, B, 1024, dtype=torch.bfloat16, device="cuda")
+    logits = torch.zeros(B, D.vocab, dtype=torch.bfloat16, device="cuda")
+    toks = bd.step(dbg_hidden=dbg, dbg_teacher=teacher.cuda(), logits_out=logits)
+    bd.check_status()
+    got = dbg.cpu()
+    for b, (o, tr, ref_lg, L) in refs.items():
+        frac = float((got[:, b] != tr).float().mean())
+        max_abs = float((got[:, b].float() - tr.float()).abs().max())
+        dl = float((logits[b].float().cpu() - ref_lg).abs().max())
+        print(f"B=64, seq {b} (context {L}): {frac:.3%} of elements differ, max abs {max_abs}, max |dlogit| {dl:.4f}")
+        assert frac < FRAC_TOL and max_abs <= LAYER_ABS_TOL and dl <= LOGIT_TOL
+        st, sr = bd.dn_states[b].cpu(), o.dn_states_ref_layout()
+        assert float((st - sr).norm() / sr.norm()) <= STATE_REL_TOL
+        page = int(bd.block_table[b, L // 64])
+        k_new = bd.k_pages[:, page, :, L % 64].float().cpu()                   # the appended K row of all six attention layers
+        assert float((k_new - torch.stack(o.k_cache)[:, :, L].float()).abs().max()) <= 0.0625
+    assert bool(((toks >= 0) & (toks < D.vocab)).all())
+    assert int(bd.positions[0]) == 2050 and int(bd.positions[63]) == 2101
+
+
+def test_batched_position_beyond_the_cache_is_refused(full_weights_cpu):
+    """Positions advance on the device.  The host refuses a step once its own bound reaches max_ctx; a position written
+    behind its back is caught by the kernels, which skip that sequence (no K/V write, no advance), leave the others
+    alone and set the sticky status word."""
+    from qwen35_b200._capi import Qwen35Error
+    from qwen35_b200.config import QWEN35_0P8B as D
+    from qwen35_b200.model import BatchedDecoder
+    from qwen35_b200.weights import make_token_ids, weights_to
+    wg = weights_to(full_weights_cpu, "cuda")
+    bd = BatchedDecoder(wg, batch=2, max_ctx=64)
+    for b in range(2):
+        bd.prefill(b, make_token_ids(60, 40 + b, D.vocab).cuda())
+    for _ in range(4):
+        bd.step()
+    bd.check_status()
+    assert bd.positions.tolist() == [64, 64]
+    with pytest.raises(ValueError):
+        bd.step()                                   # the host's bound: position 64 does not fit a 64-token cache
+    # behind the host's back: sequence 1 claims a position far outside its page-table row
+    bd2 = BatchedDecoder(wg, batch=2, max_ctx=64)
+    for b in range(2):
+        bd2.prefill(b, make_token_ids(20, 40 + b, D.vocab).cuda())
+    ref = BatchedDecoder(wg, batch=2, max_ctx=64)
+    for b in range(2):
+        ref.prefill(b, make_token_ids(20, 40 + b, D.vocab).cuda())
+    k_before = bd2.k_pages.clone()
+    bd2.positions[1] = 5000
+    t = bd2.step().clone()
+    t_ref = ref.step().clone()
+    with pytest.raises(Qwen35Error):
+        bd2.check_status()
+    assert int(bd2.positions[1]) == 5000 and int(bd2.positions[0]) == 21          # skipped sequence did not advance
+    assert int(t[0]) == int(t_ref[0])                                              # its neighbour is unaffected
+    assert torch.equal(bd2.k_pages[:, 1], k_before[:, 1])                         # nothing written into sequence 1's page
+    import ctypes as C
+    bd2._lib.qwen35_b200_clear_status(C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    bd2.check_status()

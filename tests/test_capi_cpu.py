@@ -76,3 +76,50 @@ def test_calls_fail_loudly_without_a_device():
     assert st != 0
     with pytest.raises(_capi.Qwen35Error):
         _capi.check(st, "status")
+
+
+def _header_params():
+    """name -> parameter count of every function include/qwen35_b200.h declares."""
+    text = open(os.path.join(ROOT, "include", "qwen35_b200.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    out = {}
+    for m in re.finditer(r"^\s*(?:const\s+)?(?:int|long long|size_t|char\s*\*|void)\s*\*?\s*(\w+)\s*\(([^)]*)\)\s*;", text, flags=re.M | re.S):
+        params = [p for p in (" ".join(x.split()) for x in m.group(2).split(",")) if p and p != "void"]
+        out[m.group(1)] = params
+    return out
+
+
+def test_every_reference_launcher_is_exported_with_its_argument_list():
+    """The `extern "C"` functions the reference's binding layer declares (torch_bindings.cpp:47-119, 323-364; list kept
+    in tests/golden/reference_c_abi.json by make_c_abi_list.py): each is exported by the library and declared in the
+    header with the same number of parameters, pointer parameters in the same places."""
+    import json
+    ref = json.load(open(os.path.join(ROOT, "tests", "golden", "reference_c_abi.json")))["functions"]
+    assert len(ref) == 9
+    hdr = _header_params()
+    lib = ctypes.CDLL(_capi.LIB_PATH)
+    for fn in ref:
+        name = fn["name"]
+        assert hasattr(lib, name), f"{name}: declared by the reference's torch_bindings.cpp, not exported"
+        assert name in hdr, f"{name}: not declared in include/qwen35_b200.h"
+        assert len(hdr[name]) == len(fn["params"]), f"{name}: {len(hdr[name])} parameters here, {len(fn['params'])} in the reference"
+        for mine, (rtype, rname) in zip(hdr[name], fn["params"]):
+            if rtype == "cudaStream_t":
+                assert mine.startswith("qwen35_stream_t"), f"{name}: parameter {rname}: '{mine}' is not the stream"
+            else:
+                assert ("*" in mine) == ("*" in rtype), f"{name}: parameter {rname}: '{mine}' vs '{rtype}'"
+        assert len(_capi.SIGNATURES[name][1]) == len(fn["params"]), f"{name}: ctypes signature length"
+
+
+def test_reference_c_abi_fixture_is_current():
+    """Where the reference checkout is present, the committed list equals a fresh parse of its binding layer."""
+    src = "/root/reference/models/qwen35_0p8b/torch_bindings.cpp"
+    if not os.path.exists(src):
+        pytest.skip("reference checkout not present")
+    import importlib.util
+    import json
+    spec = importlib.util.spec_from_file_location("make_c_abi_list", os.path.join(ROOT, "tests", "golden", "make_c_abi_list.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    fresh = mod.parse_extern_c(open(src).read())
+    assert fresh == json.load(open(os.path.join(ROOT, "tests", "golden", "reference_c_abi.json")))["functions"]

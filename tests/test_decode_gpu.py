@@ -25,7 +25,8 @@ pytestmark = pytest.mark.gpu
 
 LAYER_ABS_TOL = 2.0 ** -5        # absolute bound on any layer-output element, hidden scale is 1..4
 STATE_REL_TOL = 1e-3             # DeltaNet state, relative Frobenius error
-LOGIT_NOISE = 0.30               # model-level logit bound: 2x the oracle's own 1-ulp sensitivity (0.08-0.15)
+LOGIT_TOL = 2e-2                 # teacher-forced logits (computed from the GPU's own last-layer output): the task's bound
+LOGIT_NOISE = 0.30               # free-running logits only: 2x the oracle's own 1-ulp sensitivity over 24 layers (0.08-0.15)
 
 
 @pytest.fixture(scope="module")
@@ -39,10 +40,14 @@ def ctx(full_weights_cpu):
     return dict(D=D, w=full_weights_cpu, dec=dec, Oracle=Oracle, ids=make_token_ids(64, 7, D.vocab))
 
 
-@pytest.mark.parametrize("n_prompt", [1, 3, 40])
+@pytest.mark.parametrize("n_prompt", [1, 3, 40, 648])
 def test_layer_parity_teacher_forced(ctx, n_prompt):
+    """648 = the last context length of the benchmarked pp520 + tg128 run (21 attention chunks of 31 positions)."""
     D, dec = ctx["D"], ctx["dec"]
     ids = ctx["ids"]
+    if n_prompt >= len(ids):
+        from qwen35_b200.weights import make_token_ids
+        ids = make_token_ids(n_prompt + 1, 7, D.vocab)
     o = ctx["Oracle"](ctx["w"], D, 2048)
     o.prefill(ids[:n_prompt])
     load_oracle_state(dec, o)
@@ -65,7 +70,8 @@ def test_layer_parity_teacher_forced(ctx, n_prompt):
     assert max_abs <= LAYER_ABS_TOL
     # logits of the last layer's (GPU) output: same arg-max, small deviation
     ld = (logits.cpu() - ref_logits.float()).abs()
-    assert float(ld.max()) <= LOGIT_NOISE
+    print(f"n_prompt={n_prompt}: teacher-forced max |dlogit| {float(ld.max()):.4f}")
+    assert float(ld.max()) <= LOGIT_TOL
     margin = torch.topk(ref_logits.float(), 2).values
     if float(margin[0] - margin[1]) > 2 * float(ld.max()):
         assert int(tok[0]) == int(ref_logits.argmax())
@@ -167,3 +173,49 @@ def test_argument_checks(ctx):
     with pytest.raises(TypeError):
         dec.prefill_tokens(torch.zeros(4, dtype=torch.int64, device="cuda"))
     dec.check_status()
+
+
+def test_gpu_is_as_close_to_the_exact_evaluation_as_the_reference_order_is(ctx):
+    """Two correct bf16 implementations differ where their f32 sums straddle a rounding boundary.  To show that what
+    separates the CUDA path from the oracle is that and nothing else, both are compared with a third evaluation in which
+    every projection is summed exactly (f64) and rounded once.  Layer level, teacher forced on the oracle's inputs, three
+    decode steps at different contexts: the CUDA path must not sit further from the exact values than the
+    HuggingFace-order oracle does (factor 1.5 plus a small constant for the counting noise of a handful of flips)."""
+    import copy
+    import oracle.qwen35_oracle as Q
+    from qwen35_b200.weights import make_token_ids
+    D, dec = ctx["D"], ctx["dec"]
+    tot_hf = tot_gpu = 0
+    per_layer_hf, per_layer_gpu = torch.zeros(24, dtype=torch.long), torch.zeros(24, dtype=torch.long)
+    max_hf = max_gpu = 0.0
+    for n_prompt, seed in ((5, 21), (70, 22), (200, 23)):
+        ids = make_token_ids(n_prompt + 1, seed, D.vocab)
+        o = ctx["Oracle"](ctx["w"], D, 2048)
+        o.prefill(ids[:n_prompt])
+        oe = copy.deepcopy(o)
+        load_oracle_state(dec, o)
+        o.step(int(ids[n_prompt]))
+        trace = torch.stack(o.trace)
+        teacher_rows = [None] + [trace[i][None] for i in range(23)]
+        Q.EXACT_LINEAR = True
+        try:
+            oe.step(int(ids[n_prompt]), teacher=teacher_rows)
+        finally:
+            Q.EXACT_LINEAR = False
+        exact = torch.stack(oe.trace)
+        teacher = torch.zeros(24, 1024, dtype=torch.bfloat16)
+        teacher[1:] = trace[:-1]
+        dbg = torch.zeros(24, 1024, dtype=torch.bfloat16, device="cuda")
+        dec.forced_steps(ids[n_prompt:n_prompt + 1].cuda(), dbg_hidden=dbg, dbg_teacher=teacher.cuda())
+        dec.check_status()
+        got = dbg.cpu()
+        per_layer_hf += (trace != exact).sum(dim=1)
+        per_layer_gpu += (got != exact).sum(dim=1)
+        max_hf = max(max_hf, float((trace.float() - exact.float()).abs().max()))
+        max_gpu = max(max_gpu, float((got.float() - exact.float()).abs().max()))
+    tot_hf, tot_gpu = int(per_layer_hf.sum()), int(per_layer_gpu.sum())
+    print(f"layer outputs differing from the exactly-rounded evaluation over 3 steps x 24 layers x 1024: reference-order oracle {tot_hf}, "
+          f"CUDA path {tot_gpu}; max |diff| {max_hf} vs {max_gpu}")
+    print("  per layer (oracle / CUDA):", list(zip(per_layer_hf.tolist(), per_layer_gpu.tolist())))
+    assert tot_gpu <= 1.5 * tot_hf + 64
+    assert max_gpu <= max(2 * max_hf, 2.0 ** -6)

@@ -14,7 +14,7 @@ pytestmark = pytest.mark.gpu
 
 LAYER_ABS_TOL = 2.0 ** -5
 STATE_REL_TOL = 1e-3
-LOGIT_NOISE = 0.30
+LOGIT_TOL = 2e-2                 # teacher-forced logits: the task's bound
 
 
 @pytest.fixture(scope="module")
@@ -61,7 +61,7 @@ def test_layer_parity_teacher_forced(ctx, n_prompt):
     ld = (logits.cpu() - ref_logits.float()).abs()
     print(f"nvfp4 n_prompt={n_prompt}: {exact_layers}/24 layers bit-identical, {frac:.4%} elements differ, max abs {max_abs}, max |dlogit| {float(ld.max()):.4f}")
     assert exact_layers >= 14 and frac < 0.06 and max_abs <= LAYER_ABS_TOL
-    assert float(ld.max()) <= LOGIT_NOISE
+    assert float(ld.max()) <= LOGIT_TOL
     top = torch.topk(ref_logits.float(), 2).values
     if float(top[0] - top[1]) > 2 * float(ld.max()):
         assert int(tok[0]) == int(ref_logits.argmax())
@@ -109,3 +109,29 @@ def test_reference_signature_entry_points(ctx):
     assert outs.tolist() == ref and int(tokbuf.item()) == ref[-1]
     with pytest.raises(_capi.Qwen35Error):
         _capi.check(lib.launch_decode_nvfp4(tokbuf.data_ptr(), tokbuf.data_ptr(), *common(), 11, dec.max_seq_len, 16, st), "group 16")
+
+
+def test_launch_prefill_megakernel_nvfp4(ctx):
+    """The reference's argument list (torch_bindings.cpp:104-119): the prompt in one dispatch, token-serial, LM head after
+    the last token.  Must leave the state and return the token of the extended entry point run over the same prompt."""
+    from qwen35_b200 import _capi
+    dec = ctx["dec"]
+    lib = _capi.lib()
+    ids = ctx["ids"][:9].cuda()
+    dec.reset()
+    ref_first = int(dec.forced_steps(ids)[-1])
+    ref_state, ref_k = dec._dn_states.clone(), dec._fa_k_cache[:, :, :9].clone()
+    dec.reset()
+    out = torch.zeros(1, dtype=torch.int32, device="cuda")
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    args = [ids.data_ptr(), 9, out.data_ptr(), dec._embed_weight.data_ptr(), dec._layer_weights_packed_nvfp4.data_ptr(),
+            dec._final_norm_weight.data_ptr(), dec._lm_head_weight_packed.data_ptr(), dec._lm_head_scales.data_ptr(), None, None, None, None,
+            dec._fa_k_cache.data_ptr(), dec._fa_v_cache.data_ptr(), dec._dn_states.data_ptr(), dec._conv_bufs.data_ptr(),
+            dec._hidden.data_ptr()] + [None] * 10 + [None] * 5 + [dec.max_seq_len, 32, st]
+    _capi.check(lib.launch_prefill_megakernel_nvfp4(*args), "launch_prefill_megakernel_nvfp4")
+    dec.check_status()
+    assert int(out.item()) == ref_first
+    assert torch.equal(dec._dn_states, ref_state) and torch.equal(dec._fa_k_cache[:, :, :9], ref_k)
+    args[-2] = 16
+    with pytest.raises(_capi.Qwen35Error):
+        _capi.check(lib.launch_prefill_megakernel_nvfp4(*args), "group 16")

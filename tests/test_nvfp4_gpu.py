@@ -54,3 +54,62 @@ def test_padded_rows_and_errors():
         _quantize_matrix_nvfp4(w, 48)
     with pytest.raises(TypeError):
         _quantize_matrix_nvfp4(w.float(), 32)
+
+
+# ---- against the reference's own packer kernels -------------------------------------------------------------
+# oracle/_ref/libref_nvfp4.so is the reference's NVFP4 translation unit compiled unchanged with its own flags (including
+# --use_fast_math) by oracle/Makefile; its two launchers run the reference's quantize_nvfp4_kernel and
+# quantize_nvfp4_lm_kernel (kernel_gb10_nvfp4.cu:1757-1810, 1366-1430).  Test side only: the product never loads it.
+def _reference_lib():
+    import ctypes as C
+    import os
+    from conftest import ROOT
+    path = os.path.join(ROOT, "oracle", "_ref", "libref_nvfp4.so")
+    if not os.path.exists(path):
+        pytest.skip("oracle/_ref/libref_nvfp4.so not built (make -C oracle, where the reference checkout is present)")
+    lib = C.CDLL(path)
+    vp, i = C.c_void_p, C.c_int
+    lib.launch_quantize_nvfp4_out.restype = None
+    lib.launch_quantize_nvfp4_out.argtypes = [vp, i, i, i, vp, vp, vp]
+    lib.launch_quantize_nvfp4_lm_out.restype = None
+    lib.launch_quantize_nvfp4_lm_out.argtypes = [vp, i, i, vp, vp, vp]
+    return lib
+
+
+def _model_matrices(full_weights_cpu):
+    """One matrix of every shape the 0.8B model quantises (DeltaNet qkv / z / out, attention q / k / o, gate, down) and a
+    slab of the LM head, plus the known-answer rows (ties, all-zero blocks, saturation, sub-floor values)."""
+    dn = next(l for l in full_weights_cpu["layer_data"] if l["type"] == 0)["ptrs"]
+    fa = next(l for l in full_weights_cpu["layer_data"] if l["type"] == 1)["ptrs"]
+    mats = [dn[1], dn[2], dn[9], dn[11], dn[13], fa[1], fa[2], fa[6], full_weights_cpu["lm_head_weight"][:4096]]
+    mats += [torch.from_numpy(m).bfloat16() for m in _mats()]
+    return mats
+
+
+def test_packers_equal_the_reference_kernels_byte_for_byte(full_weights_cpu):
+    import ctypes as C
+    from qwen35_b200.model import _quantize_matrix_nvfp4, _quantize_matrix_nvfp4_lm
+    ref = _reference_lib()
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    n_dec = n_tc = 0
+    for w in _model_matrices(full_weights_cpu):
+        w = w.cuda().contiguous()
+        rows, cols = w.shape
+        for group in (32, 16):
+            mine = _quantize_matrix_nvfp4(w, group)
+            p = torch.zeros_like(mine["packed"]); s = torch.zeros_like(mine["scales"])
+            ref.launch_quantize_nvfp4_out(w.data_ptr(), rows, cols, group, p.data_ptr(), s.data_ptr(), st)
+            torch.cuda.synchronize()
+            assert torch.equal(p, mine["packed"]), (tuple(w.shape), group, "packed")
+            assert torch.equal(s.view(torch.int16), mine["scales"].view(torch.int16)), (tuple(w.shape), group, "scales")
+            n_dec += 1
+        if rows % 128 == 0 and cols % 64 == 0:
+            mine = _quantize_matrix_nvfp4_lm(w)
+            p = torch.zeros_like(mine["packed"]); s = torch.zeros_like(mine["scales"])
+            ref.launch_quantize_nvfp4_lm_out(w.data_ptr(), rows, cols, p.data_ptr(), s.data_ptr(), st)
+            torch.cuda.synchronize()
+            assert torch.equal(p, mine["packed"]), (tuple(w.shape), "tc packed")
+            assert torch.equal(s, mine["scales"]), (tuple(w.shape), "tc scales")
+            n_tc += 1
+    print(f"{n_dec} decode-layout and {n_tc} tensor-core-layout packings identical to the reference kernels'")
+    assert n_dec >= 20 and n_tc >= 8

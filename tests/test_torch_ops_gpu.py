@@ -54,15 +54,31 @@ def test_ops_match_decoder_api(full_weights_cpu):
         got.append(int(out.item()))
     assert got == ref
 
-    # ---- single-dispatch bf16 prompt pass equals the token-serial mode ----
-    t_serial = bdec.prefill_tokens(ids, mode="serial")
-    st_serial = bdec._dn_states.clone()
+    # ---- single-dispatch bf16 prompt pass: the batched pass without the fused-weight table; agrees with the fused op ----
+    t_fused = bdec.prefill_tokens(ids, mode="batched")
+    st_fused = bdec._dn_states.clone()
+    t_mega = bdec.prefill_tokens(ids, mode="mega")
+    st_mega = bdec._dn_states.clone()
     bdec.reset()
     ops.prefill_bf16_mega(out, ids, bdec._embed_weight, bdec._layer_weights_packed, bdec._final_norm_weight, bdec._lm_head_weight,
                           bdec._fa_k_cache, bdec._fa_v_cache, bdec._dn_states, bdec._conv_bufs, b["hidden"], b["residual"], b["normalized"],
                           b["proj_buf"], b["proj_buf2"], b["attn_buf"], b["mlp_buf"], b["dn_out_buf"], b["beta_buf"], b["alpha_buf"],
                           b["final_normed"], b["hidden_bf16_out"], b["lm_bmv"], b["lm_bmi"])
-    assert int(out.item()) == t_serial and torch.equal(bdec._dn_states, st_serial)
+    assert int(out.item()) == t_mega and torch.equal(bdec._dn_states, st_mega)
+    assert float((st_mega[0] - st_fused[0]).norm() / st_fused[0].norm()) <= 1e-3 and 0 <= t_fused < D.vocab
+    # the C symbol of the same name with the reference's argument list (torch_bindings.cpp:354-364; cache length 2048)
+    import ctypes as C
+    from qwen35_b200 import _capi
+    bdec.reset()
+    ptr = lambda t: t.data_ptr()       # noqa: E731
+    st = _capi.lib().launch_prefill_bf16_mega(
+        ptr(ids), 40, ptr(out), ptr(bdec._embed_weight), ptr(bdec._layer_weights_packed), ptr(bdec._final_norm_weight), ptr(bdec._lm_head_weight),
+        ptr(bdec._fa_k_cache), ptr(bdec._fa_v_cache), ptr(bdec._dn_states), ptr(bdec._conv_bufs), ptr(b["hidden"]), ptr(b["residual"]),
+        ptr(b["normalized"]), ptr(b["proj_buf"]), ptr(b["proj_buf2"]), ptr(b["attn_buf"]), ptr(b["mlp_buf"]), ptr(b["dn_out_buf"]),
+        ptr(b["beta_buf"]), ptr(b["alpha_buf"]), ptr(b["final_normed"]), ptr(b["hidden_bf16_out"]), ptr(b["lm_bmv"]), ptr(b["lm_bmi"]),
+        C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    _capi.check(st, "launch_prefill_bf16_mega")
+    assert int(out.item()) == t_mega and torch.equal(bdec._dn_states, st_mega)
 
     # ---- NVFP4: token-serial prompt pass, decode_nvfp4, decode_many_nvfp4 ----
     nv_head = [dec._embed_weight, dec._layer_weights_packed_nvfp4, dec._final_norm_weight, dec._lm_head_weight_packed, dec._lm_head_scales,

@@ -95,6 +95,42 @@ def test_tree_verify_matches_path_sequential_oracle(n_ctx, n_nodes, max_depth, s
     parents = random_tree(n_nodes, max_depth, seed) if n_nodes > 1 else [-1]
     if seed == 4:
         parents = [-1] + list(range(n_nodes - 1))          # a pure chain: the tree pass equals sequential decoding
+    _check_tree_against_oracle(D, orc, tt, rng, parents, n_nodes)
+
+
+def test_tree_verify_at_the_27b_widths():
+    """The widths of the benchmarked configuration (hidden 5120, FFN 17 408, 24 q / 4 kv heads: six query heads per kv
+    head, 198 query rows per attention CTA; 48 value / 16 key DeltaNet heads; qwen35_target_graph.cpp:46-67) on a
+    two-layer model (one DeltaNet, one attention layer), a 4096-token context (32 key chunks) of random cache rows
+    loaded identically into the oracle and the GPU target, and the benchmark's 33-node tree of depth <= 8.  Same
+    assertions as the reduced-width cases: teacher-forced layer outputs, per-node states, logits, walk, commit."""
+    import dataclasses
+    from oracle.tree_verify_oracle import TreeOracle, rb
+    from qwen35_b200.tree_verify import QWEN35_27B, TreeTarget, make_random_tree_weights, random_tree
+    D = dataclasses.replace(QWEN35_27B, n_layers=2, fa_period=2, vocab=4096)
+    assert (D.hidden, D.ffn, D.q_heads, D.kv_heads, D.dn_v_heads, D.dn_k_heads) == (5120, 17408, 24, 4, 48, 16)
+    n_ctx, n_nodes = 4096, 33
+    w = make_random_tree_weights(D, 11)
+    orc = TreeOracle(D, w, n_ctx + 64)
+    g = torch.Generator().manual_seed(11)
+    orc.k = [rb(torch.randn(D.kv_heads, n_ctx, D.head_dim, generator=g)) for _ in range(D.n_fa)]
+    orc.v = [rb(torch.randn(D.kv_heads, n_ctx, D.head_dim, generator=g)) for _ in range(D.n_fa)]
+    orc.ssm = [0.01 * torch.randn(D.dn_v_heads, D.dn_dim, D.dn_dim, generator=g) for _ in range(D.n_dn)]
+    orc.conv = [0.1 * torch.randn(3, D.conv_ch, generator=g) for _ in range(D.n_dn)]
+    orc.past = n_ctx
+    wg = {"layers": [{k: v.cuda() for k, v in L.items()} for L in w["layers"]],
+          "token_embd": w["token_embd"].cuda(), "output_norm": w["output_norm"].cuda(), "output_w": w["output_w"].cuda()}
+    tt = TreeTarget(D, wg, max_ctx=n_ctx + 64)
+    for i in range(D.n_fa):
+        tt.k_cache[i, :, :n_ctx] = orc.k[i].bfloat16().cuda(); tt.v_cache[i, :, :n_ctx] = orc.v[i].bfloat16().cuda()
+    for i in range(D.n_dn):
+        tt.ssm_state[i] = orc.ssm[i].cuda(); tt.conv_state[i] = orc.conv[i].cuda()
+    tt.past = n_ctx
+    rng = np.random.default_rng(11)
+    _check_tree_against_oracle(D, orc, tt, rng, random_tree(n_nodes, 8, 11), n_nodes)
+
+
+def _check_tree_against_oracle(D, orc, tt, rng, parents, n_nodes):
     tokens = rng.integers(0, D.vocab, n_nodes)
     ref_logits, ctxs, hids = orc.verify(tokens, parents)
     teacher = torch.zeros(D.n_layers, n_nodes, D.hidden, dtype=torch.bfloat16)
@@ -307,7 +343,7 @@ def test_feature_ring_capture_and_commit():
     tt = TreeTarget(D, wg, max_ctx=256, capture_layers=layers, feat_cap=cap)
     rng = np.random.default_rng(7)
     history = []                                   # per committed position: [layer k] -> row
-    for step in range(4):                          # 4 rounds x up to 4 accepted of 9 nodes: passes the wrap at 24
+    for step in range(9):                          # 9 rounds x up to 4 accepted of 9 nodes: passes the wrap at 24
         n = 9
         parents = random_tree(n, 4, 30 + step)
         tokens = rng.integers(0, D.vocab, n)
@@ -339,12 +375,17 @@ def test_feature_ring_capture_and_commit():
             for k, il in enumerate(layers):
                 assert torch.equal(tt.target_feat[(past + d) % cap, k * D.hidden:(k + 1) * D.hidden], dbg[il, node]), (step, d, k)
     assert tt.past == len(history) and tt.past > 0
-    win = tt.feature_window(10)
-    n = min(10, tt.past)
-    assert win.shape == (n, len(layers) * D.hidden)
-    for i in range(n):
-        for k in range(len(layers)):
-            assert torch.equal(win[i, k * D.hidden:(k + 1) * D.hidden], history[tt.past - n + i][k])
+    # The largest window that is safe for 9-node trees: cap - 8 rows (the 9 rows a verify writes overwrite the oldest ring
+    # positions once the ring has wrapped; with the root accepted the next window must end 8 rows short of them).  Every
+    # row of it must be the committed position's own feature row, including those beyond the wrap-around.
+    assert tt.past > cap - 8                  # the ring has wrapped under partly rejected trees
+    for want in (10, cap - 8):
+        win = tt.feature_window(want)
+        n = min(want, tt.past)
+        assert win.shape == (n, len(layers) * D.hidden)
+        for i in range(n):
+            for k in range(len(layers)):
+                assert torch.equal(win[i, k * D.hidden:(k + 1) * D.hidden], history[tt.past - n + i][k]), (want, i, k)
 
 
 @pytest.mark.parametrize("n_ctx,n_nodes,seed", [(70, 14, 21), (130, 33, 22), (0, 5, 23)])

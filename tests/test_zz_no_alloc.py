@@ -63,3 +63,51 @@ def test_static_scratch_entry_point_matches_allocating_one(full_weights_cpu):
     st = lib.qwen35_b200_decode_steps_static(C.byref(a), dec._stream())
     assert st == 2
     assert b"32768" in lib.qwen35_b200_last_error()
+
+
+_FRESH_PROCESS = r"""
+import ctypes as C, sys
+sys.path.insert(0, {root!r}); sys.path.insert(0, {pkg!r})
+import torch
+from qwen35_b200 import _capi
+from qwen35_b200.config import QWEN35_0P8B as D
+from qwen35_b200.model import Decoder
+from qwen35_b200.weights import make_random_weights, make_token_ids, weights_to
+lib = _capi.lib()
+dec = Decoder(weights=weights_to(make_random_weights(1234, D), "cuda"), max_seq_len=256)
+ids = make_token_ids(6, 5, D.vocab).cuda()
+out = torch.zeros(6, dtype=torch.int32, device="cuda")
+stream = dec._stream()
+
+def call(pos):
+    a = dec._args(forced_ids=ids.data_ptr(), n_steps=6, out_tokens=out.data_ptr())
+    a.position = pos
+    _capi.check(lib.qwen35_b200_decode_steps_static(C.byref(a), stream), "decode_steps_static")
+    _capi.check(lib.qwen35_b200_status(stream), "status")          # synchronises; must not create the regular workspace
+
+call(0)                                   # first call on the device: module load + symbol look-up happen here
+torch.cuda.synchronize()
+assert lib.qwen35_b200_workspace_if_any() is None, "status() created the library workspace"
+free0, _ = torch.cuda.mem_get_info()
+call(6)
+_capi.check(lib.qwen35_b200_clear_status(stream), "clear_status")
+torch.cuda.synchronize()
+free1, _ = torch.cuda.mem_get_info()
+assert lib.qwen35_b200_workspace_if_any() is None, "status()/clear_status() created the library workspace"
+assert free1 == free0, f"device memory in use changed across an allocation-free call: {{free0}} -> {{free1}}"
+print("NOALLOC_OK", out.tolist())
+"""
+
+
+def test_static_entry_point_and_status_allocate_nothing_in_a_fresh_process():
+    """A process that only ever uses the allocation-free entry point, and reads and clears the status the way the header tells it
+    to, must never make the library allocate: the regular workspace does not come into being and the device's free
+    memory is the same before and after a call.  Runs in a child process, because every other test of this session has
+    already made the library create its workspace."""
+    import os
+    import subprocess
+    import sys
+    from conftest import ROOT
+    code = _FRESH_PROCESS.format(root=ROOT, pkg=os.path.join(ROOT, "lucebox-hub_b200"))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "NOALLOC_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-4000:]
