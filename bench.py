@@ -311,6 +311,40 @@ def batched_decode_bench(weights_gpu, dev, rank, n_seq, ctx, n_steps, kernel_tab
     return n_seq * n_steps / (ms * 1e-3), ms / n_steps, bytes_step
 
 
+def parity_section(dec, dev):
+    """Greedy-path agreement with the committed fixture of the reference's ground truth (the transformers model on the same
+    seeded weights and prompt, tests/golden/qwen35_0p8b_p520_g128_f32.npz): length of the common prefix of the free-running
+    128-token path, teacher-forced arg-max agreement, and for every teacher-forced disagreement the fixture's own top-2
+    margin in bf16 last places of the top logit (an exact tie is 0).  Reads the fixture only; runs no CPU model."""
+    import numpy as np
+    path = os.path.join(ROOT, "tests", "golden", "qwen35_0p8b_p%d_g%d_f32.npz" % (PROMPT, GEN))
+    if not os.path.exists(path):
+        return {"unavailable": "no fixture for pp%d + tg%d" % (PROMPT, GEN)}
+    g = np.load(path)
+    ids = torch.from_numpy(g["prompt_ids"]).to(dev)
+    gold = g["tokens"].tolist()
+    first = dec.prefill_tokens(ids)
+    got = [first] + dec.step_many(first, GEN - 1).tolist()
+    prefix = next((i for i, (a, b) in enumerate(zip(got, gold)) if a != b), len(gold))
+    first = dec.prefill_tokens(ids)
+    forced = torch.tensor(gold[:-1], dtype=torch.int32, device=dev)
+    tf = [first] + dec.forced_steps(forced).tolist()
+    dec.check_status()
+    top = g["top_vals"].astype(np.float64)
+    ulp = 2.0 ** (np.floor(np.log2(np.abs(top[:, 0]))) - 7)            # one bf16 last place of the top logit
+    margin_ulps = (top[:, 0] - top[:, 1]) / ulp
+    agree = np.array([a == b for a, b in zip(tf, gold)])
+    bad = [{"step": int(i), "fixture_margin_ulps": float(margin_ulps[i])} for i in np.nonzero(~agree)[0]]
+    clear = margin_ulps > 2.0
+    return {"fixture": "transformers 5.5.0 Qwen3_5ForCausalLM, f32 DeltaNet state, weights seed %d, prompt seed %d" % (int(g["seed_weights"]), int(g["seed_ids"])),
+            "free_running_prefix": int(prefix), "of": len(gold),
+            "teacher_forced_agreement": float(agree.mean()),
+            "teacher_forced_agreement_margin_gt_2ulp": float(agree[clear].mean()) if clear.any() else None,
+            "fixture_steps_with_exact_tie": int((margin_ulps == 0).sum()), "fixture_steps_within_1_ulp": int((margin_ulps <= 1).sum()),
+            "fixture_min_margin_ulps": float(margin_ulps.min()),
+            "teacher_forced_disagreements": bad[:24]}
+
+
 def host_cores() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -501,6 +535,7 @@ def run_ours(args):
     e2e_ms = e0.elapsed_time(e1)
     clocks = sampler.stop()
     dec.check_status()
+    parity = parity_section(dec, dev) if rank == 0 else None
 
     sweep = None
     if args.prefill_sweep and rank == 0:
@@ -572,8 +607,8 @@ def run_ours(args):
                     "path": "Decoder.step(): one launch_decode + one 4-byte device->host read per token"},
             "gpu_launches": launches, "clocks": clocks,
         }
-        if batched:
-            line["batched_decode"] = batched
+        if parity is not None:
+            line["parity"] = parity
         if sweep:
             line["prefill_sweep"] = sweep
         if tree:
@@ -586,9 +621,12 @@ def run_ours(args):
             line["cpu_baseline"] = cpu_baseline(w_cpu, ids_cpu, 16, use_hf=False)
             if batched:
                 # the CPU runs the sequences one after another, so its aggregate rate is its single-sequence rate
-                batched["cpu_baseline"] = dict(line["cpu_baseline"], sample="single-sequence decode rate of the bs=1 sample (the CPU path has no batching); context 520 instead of 2048")
+                batched["cpu_baseline"] = {"value": line["cpu_baseline"]["value"], "unit": "tok/s", "cores": line["cpu_baseline"]["cores"], "kind": "port",
+                                           "sample": "single-sequence decode rate of the bs=1 sample (the CPU path has no batching); context 520 instead of 2048"}
             if tree:
                 tree["cpu_baseline"] = tree_cpu_baseline()
+        if batched:
+            line["batched_decode"] = batched          # last key: the per-N aggregate stays in the tail of the line
         print(json.dumps(line))
     if world > 1:
         torch.distributed.destroy_process_group()

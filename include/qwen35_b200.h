@@ -85,8 +85,8 @@ typedef struct {
     int n_steps;
     int lm_last_only;          /* 1 = run the LM head only after the last step */
     int dbg_num_layers;        /* 0 = all 24; N>0 stops after N layers (debug) */
-    unsigned long long* dbg_time; /* optional device u64 [25][12]: per-stage %globaltimer stamps of one CTA, last step */
-    int dbg_time_cta;
+    unsigned long long* dbg_time; /* optional device u64 [grid][25][12]: per-stage time stamps of every CTA, last step */
+    int dbg_time_cta;             /* -2: stamps are SM cycle counts (clock64, exact within a CTA); otherwise %globaltimer ns */
 } Qwen35DecodeArgs;
 
 int qwen35_b200_decode_steps(const Qwen35DecodeArgs* args, qwen35_stream_t stream);
@@ -412,6 +412,19 @@ int qwen35_b200_gemm_bf16(const void* A, int lda, const void* B, int b_rows, voi
  * K a multiple of 256; rows of W beyond w_rows read as zero. */
 int qwen35_b200_gemm_q4k(const void* A, int lda, const void* W, int w_rows, void* C, int ldc, const void* R, int ldr,
                          int M, int N, int K, int epilogue, int up_row_offset, qwen35_stream_t stream);
+
+/* NVFP4 block-scaled GEMM on the tensor cores (tcgen05.mma kind::mxf4nvf4, 16-element blocks, UE4M3 scales, f32 accumulate):
+ * C[tokens, n_rows] = alpha * (A_q . W_q^T).  Replaces the reference's cuBLASLt NVFP4 calls: the FP4 LM head
+ * (kernel_gb10_nvfp4.cu:277-473, 1894-1997, which quantises the activation to FP4 as well) and the NVFP4 prefill projections
+ * (cublaslt_nvfp4_bf16_gemm, prefill.cu:1020-1155).  Both operands are in the layout of launch_quantize_nvfp4_lm_out: packed
+ * nibbles [rows, K/2] and scale atoms of 512 bytes (128 rows x 4 scales), atoms of a 128-row block consecutive along K.
+ * Weights need n_rows % 128 == 0 and K % 256 == 0.  Activations are packed by qwen35_b200_quantize_act_nvfp4 (bf16 [tokens, K]
+ * in; rows are padded to a multiple of 128 with zeros; qwen35_b200_nvfp4_act_bytes gives the two buffer sizes).
+ * C is bf16 (one rounding; optional bf16 residual R added after it) or, with out_f32 != 0, f32 without rounding. */
+size_t qwen35_b200_nvfp4_act_bytes(int tokens, int K, size_t* scales_bytes);
+int qwen35_b200_quantize_act_nvfp4(const void* x, int tokens, int K, void* packed_out, void* scales_out, qwen35_stream_t stream);
+int qwen35_b200_gemm_nvfp4(const void* a_packed, const void* a_scales, int tokens, const void* w_packed, const void* w_scales, int n_rows,
+                           int K, float alpha, void* C, int ldc, int out_f32, const void* R, int ldr, qwen35_stream_t stream);
 
 /* No counterpart in the reference.  qwen35_b200_decode_steps for callers that must not allocate: an
  * inference server that hands all device memory to its own pool at start-up (a later cudaMalloc inside a

@@ -71,22 +71,33 @@ __device__ __forceinline__ void load_layer(const void* table, int layer, LayerW&
     }
 }
 
+// Work split of one CTA over the stages: contiguous ranges [begin, end) of tiles / units / row pairs.  The bounds need a
+// 64-bit multiply and divide each, so they are computed once per launch and kept in shared memory.
+enum PartIdx { PT_A_DN0, PT_A_DN1, PT_A_FA0, PT_A_FA1, PT_C0, PT_C1, PT_D0, PT_D1, PT_E0, PT_E1, PT_PAIR0, PT_PAIR1, PT_CS0, PT_CS1,
+               PT_LM0, PT_LM1, PT_LMB0, PT_LMB1, PT_COUNT };
+
 struct Smem {
     // ring first: 16-byte aligned slots
     unsigned char ring[NSLOTS * SLOT_BYTES];
     unsigned long long full[NSLOTS];
     unsigned long long empty[NSLOTS];
+    unsigned long long side_go;                  // consumers -> service warp, once per layer: the layer's side work may start
+    unsigned long long side_done;                // service warp -> consumers: it is done and fenced
     LayerW layers[NUM_LAYERS];
     __align__(16) bf16 x[INTER];                 // GEMV input of the current stage
     __align__(16) bf16 h[HIDDEN];                // raw layer input (residual of stage C)
     __align__(16) bf16 h1[HIDDEN];               // raw mixer output (residual of stage E)
     float part[512];                             // cross-warp partial sums; attention chunk statistics
+    uint32_t stage[64];                          // packed outputs of a GEMV stage, published by one coalesced store
+    uint32_t stage_b[NCONS_WARPS];               // DeltaNet recurrence outputs
     float red[NCONS_WARPS];
-    uint32_t stage[64];                          // packed outputs of a stage, published by one coalesced store
-    __align__(16) float qk[2][2][DN_K];
-    float hd[2][2];
+    __align__(16) float qk[2][2][DN_K];          // DeltaNet: normalised q and k of the (at most two) heads this CTA works on
+    float hd[2][2];                              // their beta and decay
+    int pt[PT_COUNT];                            // this CTA's share of every stage, computed once (see PartIdx)
+    int lm_row0[256];                            // first vocabulary row of every CTA's LM-head share (arg-max merge)
     __align__(16) float q[FA_GQA][FA_HEAD_DIM];
     __align__(16) float kcur[FA_HEAD_DIM];
+    __align__(16) uint32_t vcur[FA_HEAD_DIM / 2];  // the new value row (packed bf16) of the CTA whose chunk holds the current position
     __align__(16) float p[FA_GQA][ATT_CHUNK_MAX]; // scores, then probabilities, of this CTA's chunk; then the merge's group sums
     float ml[FA_GQA][2];
     int abort_flag;
@@ -104,7 +115,8 @@ __device__ __forceinline__ unsigned long long gtime() {
     } while (0)
 #define Q35_STAMP(k)                                                                                   \
     do {                                                                                               \
-        if (a.dbg_time && last_step && tid == 0) a.dbg_time[((size_t)b * 25 + stamp_row) * 12 + (k)] = gtime(); \
+        if (a.dbg_time && last_step && tid == 0)                                                       \
+            a.dbg_time[((size_t)b * 25 + stamp_row) * 12 + (k)] = (a.dbg_time_cta == -2) ? (unsigned long long)clock64() : gtime(); \
     } while (0)
 
 __device__ __forceinline__ unsigned epoch_of(const DecodeArgs& a, int step, int slot) {
@@ -121,7 +133,6 @@ constexpr int FP4_LM_BLOCKS = VOCAB / 128;          // LM head (tensor-core layo
 
 template <bool FP4>
 __device__ __forceinline__ void produce(const DecodeArgs& a, Smem& s, Ring ring, const Abort& ab) {
-    const int b = blockIdx.x, G = gridDim.x;
     const u64 pol = l2_policy_evict_first();
     long long next_t = clock64();
     const long long period = a.tma_period;
@@ -149,7 +160,7 @@ __device__ __forceinline__ void produce(const DecodeArgs& a, Smem& s, Ring ring,
         for (int layer = 0; layer < n_layers; ++layer) {
             const LayerW& L = s.layers[layer];
             if (L.type == 0) {
-                for (int u = part_begin(TILES_A_DN, b, G); u < part_begin(TILES_A_DN, b + 1, G); ++u) {
+                for (int u = s.pt[PT_A_DN0]; u < s.pt[PT_A_DN1]; ++u) {
                     const int v = u * 8;
                     if (v < DN_CONV_CH) issue_rows(L.p[W_A0], L.p[W_A0S], v, 8, HIDDEN);
                     else if (v < DN_CONV_CH + DN_V_SIZE) issue_rows(L.p[W_A1], L.p[W_A1S], v - DN_CONV_CH, 8, HIDDEN);
@@ -157,27 +168,27 @@ __device__ __forceinline__ void produce(const DecodeArgs& a, Smem& s, Ring ring,
                     else issue_rows(L.p[W_A3], nullptr, v - DN_CONV_CH - DN_V_SIZE - DN_HEADS, 8, HIDDEN);
                 }
             } else {
-                for (int u = part_begin(TILES_A_FA, b, G); u < part_begin(TILES_A_FA, b + 1, G); ++u) {
+                for (int u = s.pt[PT_A_FA0]; u < s.pt[PT_A_FA1]; ++u) {
                     const int v = u * 8;
                     if (v < FA_QPROJ) issue_rows(L.p[W_A0], L.p[W_A0S], v, 8, HIDDEN);
                     else if (v < FA_QPROJ + FA_KV_SIZE) issue_rows(L.p[W_A1], L.p[W_A1S], v - FA_QPROJ, 8, HIDDEN);
                     else issue_rows(L.p[W_A2], L.p[W_A2S], v - FA_QPROJ - FA_KV_SIZE, 8, HIDDEN);
                 }
             }
-            for (int u = part_begin(TILES_C, b, G); u < part_begin(TILES_C, b + 1, G); ++u) issue_rows(L.p[W_OUT], L.p[W_OUTS], u * 4, 4, 2048);
-            for (int u = part_begin(UNITS_D, b, G); u < part_begin(UNITS_D, b + 1, G); ++u) {
+            for (int u = s.pt[PT_C0]; u < s.pt[PT_C1]; ++u) issue_rows(L.p[W_OUT], L.p[W_OUTS], u * 4, 4, 2048);
+            for (int u = s.pt[PT_D0]; u < s.pt[PT_D1]; ++u) {
                 issue_rows(L.p[W_GATE], L.p[W_GATES], u * 8, 8, HIDDEN);
                 issue_rows(L.p[W_UP], L.p[W_UPS], u * 8, 8, HIDDEN);
             }
-            for (int u = part_begin(TILES_E, b, G); u < part_begin(TILES_E, b + 1, G); ++u) issue_rows(L.p[W_DOWN], L.p[W_DOWNS], u * 2, 2, INTER);
+            for (int u = s.pt[PT_E0]; u < s.pt[PT_E1]; ++u) issue_rows(L.p[W_DOWN], L.p[W_DOWNS], u * 2, 2, INTER);
         }
         if (!a.lm_last_only || step == a.n_steps - 1) {
             if (!FP4) {
-                for (int u = part_begin(TILES_LM, b, G); u < part_begin(TILES_LM, b + 1, G); ++u)
+                for (int u = s.pt[PT_LM0]; u < s.pt[PT_LM1]; ++u)
                     issue((const char*)a.lm_head + (size_t)u * SLOT_BYTES, SLOT_BYTES, nullptr, 0);
             } else {
                 // per 128-row block: its 8 KB of swizzled E4M3 scales, then four 32-row tiles of packed nibbles
-                for (int blk = part_begin(FP4_LM_BLOCKS, b, G); blk < part_begin(FP4_LM_BLOCKS, b + 1, G); ++blk) {
+                for (int blk = s.pt[PT_LMB0]; blk < s.pt[PT_LMB1]; ++blk) {
                     issue((const char*)a.lm_scales + (size_t)blk * 8192, 8192, nullptr, 0);
                     for (int q = 0; q < 4; ++q) issue((const char*)a.lm_head + ((size_t)blk * 128 + q * 32) * 512, 16384, nullptr, 0);
                 }
@@ -199,18 +210,18 @@ __device__ __forceinline__ void produce(const DecodeArgs& a, Smem& s, Ring ring,
 // consumer helpers
 // ------------------------------------------------------------------------------------------------
 // K = 1024 rows, 8 per tile: four tiles in flight per CTA, warp w takes tile w/4, rows 2(w%4), +1.
-// NMAT = 2 pairs a gate tile with an up tile.  epi(first_row_of_pair, sums[NMAT][2]) runs on lane 0.
+// xq: this lane's activations, packed bf16, chunk j = elements [(32 j + lane) 8, +8) -- the same split as the 16-byte
+// chunks of a weight row, so a chunk of weights meets its chunk of activations in one dot8m.
+// NMAT = 2 pairs a gate tile with an up tile.  epi(row, sums[NMAT]) runs on lane 0 for the first row of the pair and on
+// lane 16 for the second.
 template <int NMAT, typename Epi>
-__device__ __forceinline__ void consume_k1024(Ring& ring, int n_units, const bf16* xs, const Abort& ab, Epi epi) {
+__device__ __forceinline__ void consume_k1024(Ring& ring, int n_units, const uint4 (&xq)[4], const Abort& ab, Epi epi) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float x[32];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) unpack8(*reinterpret_cast<const uint4*>(xs + (j * 32 + lane) * 8), x + 8 * j);
     const unsigned t0 = ring.t;
     for (int g = 0; g < n_units; g += 4) {
         const int ui = g + (warp >> 2);
         if (ui < n_units) {
-            float acc[NMAT][2];
+            float acc[NMAT];
 #pragma unroll
             for (int m = 0; m < NMAT; ++m) {
                 const unsigned tile = t0 + (unsigned)(ui * NMAT + m);
@@ -219,14 +230,15 @@ __device__ __forceinline__ void consume_k1024(Ring& ring, int n_units, const bf1
                 uint4 w0[4], w1[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) { w0[j] = lds128(base + j * 512); w1[j] = lds128(base + 2048 + j * 512); }
-                float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) { a0 = dot8(w0[j], x + 8 * j, a0); a1 = dot8(w1[j], x + 8 * j, a1); }
-                acc[m][0] = warp_sum(a0);
-                acc[m][1] = warp_sum(a1);
+                // four independent accumulation chains per warp
+                float a0 = dot8m(w0[0], xq[0], 0.f), a1 = dot8m(w0[1], xq[1], 0.f);
+                float b0 = dot8m(w1[0], xq[0], 0.f), b1 = dot8m(w1[1], xq[1], 0.f);
+                a0 = dot8m(w0[2], xq[2], a0); a1 = dot8m(w0[3], xq[3], a1);
+                b0 = dot8m(w1[2], xq[2], b0); b1 = dot8m(w1[3], xq[3], b1);
+                acc[m] = warp_sum2(a0 + a1, b0 + b1);
                 if (lane == 0) mbar_arrive(ring.empty_bar(tile), 4);
             }
-            if (lane == 0) epi(ui * 8 + 2 * (warp & 3), acc);
+            if ((lane & 15) == 0) epi(ui * 8 + 2 * (warp & 3) + (lane >> 4), acc);
         }
     }
     ring.t = t0 + (unsigned)(n_units * NMAT);
@@ -285,15 +297,16 @@ __device__ __forceinline__ void load_x32(const bf16* xs, int e0, float* x) {
 // NVFP4 version of consume_k1024: a row is 512 bytes of nibbles, lane l owns elements [32 l, 32 l + 32), which
 // is exactly one scale group, so the scale is applied once per (row, lane) after the dot product.
 template <int NMAT, typename Epi>
-__device__ __forceinline__ void consume_k1024_fp4(Ring& ring, int n_units, const bf16* xs, const Abort& ab, Epi epi) {
+__device__ __forceinline__ void consume_k1024_fp4(Ring& ring, int n_units, const uint4 (&xc)[4], const Abort& ab, Epi epi) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float x[32];
-    load_x32(xs, 32 * lane, x);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) unpack8(xc[j], x + 8 * j);
     const unsigned t0 = ring.t;
     for (int g = 0; g < n_units; g += 4) {
         const int ui = g + (warp >> 2);
         if (ui < n_units) {
-            float acc[NMAT][2];
+            float acc[NMAT];
 #pragma unroll
             for (int m = 0; m < NMAT; ++m) {
                 const unsigned tile = t0 + (unsigned)(ui * NMAT + m);
@@ -303,11 +316,10 @@ __device__ __forceinline__ void consume_k1024_fp4(Ring& ring, int n_units, const
                 const uint32_t sbase = ring.slot_addr(tile) + FP4_SCALE_OFF + r0 * 64u + (uint32_t)lane * 2u;
                 const uint4 p0 = lds128(base), p1 = lds128(base + 512);
                 const float s0 = lds_half(sbase), s1 = lds_half(sbase + 64);
-                acc[m][0] = warp_sum(dot32_fp4(p0, x) * s0);
-                acc[m][1] = warp_sum(dot32_fp4(p1, x) * s1);
+                acc[m] = warp_sum2(dot32_fp4(p0, x) * s0, dot32_fp4(p1, x) * s1);
                 if (lane == 0) mbar_arrive(ring.empty_bar(tile), 4);
             }
-            if (lane == 0) epi(ui * 8 + 2 * (warp & 3), acc);
+            if ((lane & 15) == 0) epi(ui * 8 + 2 * (warp & 3) + (lane >> 4), acc);
         }
     }
     ring.t = t0 + (unsigned)(n_units * NMAT);
@@ -322,14 +334,89 @@ __device__ __forceinline__ void poll4(const u64* p, int stride, uint32_t epoch, 
     poll_n<4>(p, stride, 4, epoch, ab, o);
 }
 
-// RMSNorm(1+w) of 1024 values held one pair per consumer thread; writes bf16 to xs.
-__device__ __forceinline__ void rmsnorm_pair(uint32_t raw, const bf16* w, bf16* xs, float* s_red) {
+// N flagged words at arbitrary addresses, all loads of a round in flight together.
+template <int N>
+__device__ __forceinline__ void poll_ptrs(const u64* const (&p)[N], uint32_t epoch, const Abort& ab, uint32_t (&o)[N]) {
+    u64 v[N];
+    unsigned pending = 0;
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = ld_word(p[i]);
+#pragma unroll
+    for (int i = 0; i < N; ++i) if ((uint32_t)(v[i] >> 32) != epoch) pending |= 1u << i;
+    unsigned it = 0;
+    while (pending && !ab.on()) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) if (pending & (1u << i)) v[i] = ld_word(p[i]);
+#pragma unroll
+        for (int i = 0; i < N; ++i) if ((pending & (1u << i)) && (uint32_t)(v[i] >> 32) == epoch) pending &= ~(1u << i);
+        if (++it > POLL_LIMIT || ((it & 4095u) == 0 && ld_volatile(ab.g_err) != 0)) { ab.raise(ERR_BARRIER_TIMEOUT); break; }
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i) o[i] = (uint32_t)v[i];
+}
+
+// Hidden-state hand-off: every consumer thread fetches one flagged word of a [1024] bf16 vector and parks the payload in
+// shared memory; the caller's cons_sync() hands them to everybody.  (Fewer polling warps with more words each were
+// measured slower: 4 warps -7 %, 2 warps -8 % on tg128.)
+__device__ __forceinline__ void fetch_vec1024(const u64* src, uint32_t epoch, bf16* dst, const Abort& ab) {
     const int t = threadIdx.x;
-    const float x0 = bf_lo(raw), x1 = bf_hi(raw);
-    const float tot = cons_block_sum(x0 * x0 + x1 * x1, s_red);
-    const float r = rsqrt_ieee(tot * (1.0f / HIDDEN) + RMS_EPS);
-    const uint32_t wr = __ldg(reinterpret_cast<const uint32_t*>(w) + t);
-    reinterpret_cast<uint32_t*>(xs)[t] = pack_bf16x2((x0 * r) * (1.0f + bf_lo(wr)), (x1 * r) * (1.0f + bf_hi(wr)));
+    reinterpret_cast<uint32_t*>(dst)[t] = poll_word(src + t, epoch, ab);
+}
+
+// Which 16-byte chunks of a [1024] bf16 vector a lane holds.  Interleaved (bf16 weights): chunk j = elements [(32 j + lane) 8, +8),
+// the split of a weight row's 16-byte chunks over the lanes.  Contiguous (NVFP4 weights): elements [32 lane + 8 j, +8), one
+// 32-element scale group per lane.
+template <bool CONTIG>
+__device__ __forceinline__ int lane_chunk(int j) { return CONTIG ? (int)(threadIdx.x & 31) * 4 + j : j * 32 + (int)(threadIdx.x & 31); }
+
+template <bool CONTIG>
+__device__ __forceinline__ void load_lane_chunks(const bf16* w, uint4 (&out)[4]) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) out[j] = __ldg(reinterpret_cast<const uint4*>(w) + lane_chunk<CONTIG>(j));
+}
+
+// RMSNorm(1+w) of the raw 1024-vector `hs` in shared memory, evaluated by every warp for itself: a lane reads the 32
+// values of its own chunks, the warp sums the squares with one butterfly (so every warp gets the same bits), and the lane
+// keeps its normalised values packed in registers -- exactly the operand consume_k1024 wants.  No block-wide reduction,
+// no second trip through shared memory.
+template <bool CONTIG>
+__device__ __forceinline__ void norm_to_regs(const bf16* hs, const uint4 (&wn)[4], uint4 (&xq)[4]) {
+    uint4 hq[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) hq[j] = *reinterpret_cast<const uint4*>(hs + lane_chunk<CONTIG>(j) * 8);
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t w[4] = {hq[j].x, hq[j].y, hq[j].z, hq[j].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) { ss = fmaf(bf_lo(w[k]), bf_lo(w[k]), ss); ss = fmaf(bf_hi(w[k]), bf_hi(w[k]), ss); }
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrt_ieee(ss * (1.0f / HIDDEN) + RMS_EPS);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t h[4] = {hq[j].x, hq[j].y, hq[j].z, hq[j].w};
+        const uint32_t w[4] = {wn[j].x, wn[j].y, wn[j].z, wn[j].w};
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            o[k] = pack_bf16x2((bf_lo(h[k]) * r) * (1.0f + bf_lo(w[k])), (bf_hi(h[k]) * r) * (1.0f + bf_hi(w[k])));
+        xq[j] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+// Split of the context over CTAs in an attention layer: chunks of >= 32 positions, CTA (kv head, chunk) owns one chunk.
+struct AttGeom { int nchunk, clen, kvh, chunk, j0, j1; bool att_cta, owns_pos; };
+__device__ __forceinline__ AttGeom att_geom(int pos, int b, int G) {
+    AttGeom g;
+    const int Lc = pos + 1;
+    g.nchunk = (Lc + 31) / 32;
+    { const int cap = min(ATT_MAX_CHUNKS, G / FA_KV_HEADS); if (g.nchunk > cap) g.nchunk = cap; }
+    g.clen = (Lc + g.nchunk - 1) / g.nchunk;            // <= ATT_CHUNK_MAX by the host-side limit on max_seq_len
+    g.att_cta = b < FA_KV_HEADS * g.nchunk;
+    g.kvh = b / g.nchunk; g.chunk = b % g.nchunk;
+    g.j0 = g.chunk * g.clen; g.j1 = min(Lc, g.j0 + g.clen);
+    g.owns_pos = g.att_cta && pos >= g.j0 && pos < g.j1;
+    return g;
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -351,9 +438,17 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
             mbar_init(smem_u32(&s.full[i]), 1);
             mbar_init(smem_u32(&s.empty[i]), NCONS_WARPS);
         }
+        mbar_init(smem_u32(&s.side_go), 1);
+        mbar_init(smem_u32(&s.side_done), 1);
         mbar_fence_init();
     }
     if (tid < NUM_LAYERS) load_layer<FP4>(a.layers, tid, s.layers[tid]);
+    if (tid >= 32 && tid < 32 + PT_COUNT) {
+        const int i = tid - 32;
+        constexpr int n_of[PT_COUNT / 2] = {TILES_A_DN, TILES_A_FA, TILES_C, UNITS_D, TILES_E, DN_V_SIZE / 2, DN_CONV_CH / 2, TILES_LM, FP4_LM_BLOCKS};
+        s.pt[i] = part_begin(n_of[i >> 1], b + (i & 1), G);
+    }
+    if (tid >= 64 && tid < 64 + 256 && tid - 64 < G) s.lm_row0[tid - 64] = FP4 ? part_begin(FP4_LM_BLOCKS, tid - 64, G) * 128 : part_begin(TILES_LM, tid - 64, G) * 8;
     __syncthreads();
 
     Abort ab{&s.abort_flag, &ws->err};
@@ -362,10 +457,60 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
     if (warp == NCONS_WARPS) {
         if (lane == 0) produce<FP4>(a, s, ring, ab);
         __syncwarp();
+    } else if (warp == NCONS_WARPS + 1) {
+        // ---- service warp: memory updates that need a fence, taken off the consumers' path ----
+        // DeltaNet layer: the conv-window shift of this CTA's channel pairs.  Once the consumers have read all of `o`, every
+        // CTA has finished the layer's stage B and nobody reads the old window any more.
+        // Attention layer: the CTA whose chunk holds the current position appends the new K / V row to the cache (the
+        // consumers use the copies in shared memory for this token).
+        // A fence that orders such stores before this CTA's next publication costs more than a microsecond; here it delays
+        // nobody: the consumers only check, just before they publish the layer's output, that it has completed.
+        const int n_layers = a.dbg_num_layers > 0 ? a.dbg_num_layers : NUM_LAYERS;
+        unsigned n_side = 0;
+        for (int step = 0; step < a.n_steps; ++step) {
+            int i_dn = 0, i_fa = 0;
+            const int pos = a.position + step;
+            for (int layer = 0; layer < n_layers; ++layer, ++n_side) {
+                const unsigned ep = epoch_of(a, step, layer);
+                mbar_wait(smem_u32(&s.side_go), n_side & 1u, ab);
+                bool stored = false;
+                if (s.layers[layer].type == 0) {
+                    float* conv = a.conv_bufs + (size_t)i_dn * DN_CONV_CH * 4;
+                    for (int c = s.pt[PT_CS0] + lane; c < s.pt[PT_CS1]; c += 32) {
+                        const uint32_t xw = poll_word(&ws->xa[c], ep, ab);
+                        const float4 c0 = ld_cg(reinterpret_cast<const float4*>(conv) + 2 * c);
+                        const float4 c1 = ld_cg(reinterpret_cast<const float4*>(conv) + 2 * c + 1);
+                        reinterpret_cast<float4*>(conv)[2 * c] = make_float4(c0.y, c0.z, c0.w, bf_lo(xw));
+                        reinterpret_cast<float4*>(conv)[2 * c + 1] = make_float4(c1.y, c1.z, c1.w, bf_hi(xw));
+                        stored = true;
+                    }
+                    ++i_dn;
+                } else {
+                    const AttGeom ag = att_geom(pos, b, G);
+                    if (ag.owns_pos) {
+                        const size_t row = ((size_t)i_fa * FA_KV_HEADS + ag.kvh) * a.max_seq_len + pos;
+                        uint32_t* krow = reinterpret_cast<uint32_t*>(a.k_cache + row * FA_HEAD_DIM);
+                        uint32_t* vrow = reinterpret_cast<uint32_t*>(a.v_cache + row * FA_HEAD_DIM);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            const int wd = lane + 32 * i;
+                            krow[wd] = pack_bf16x2(s.kcur[2 * wd], s.kcur[2 * wd + 1]);
+                            vrow[wd] = s.vcur[wd];
+                        }
+                        stored = true;
+                    }
+                    ++i_fa;
+                }
+                if (stored) __threadfence();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&s.side_done), 1);
+            }
+        }
     } else {
         // =========================== consumers ===========================
         int tok = a.token_in ? __ldg(a.token_in) : a.token_imm;
         const int n_layers = a.dbg_num_layers > 0 ? a.dbg_num_layers : NUM_LAYERS;
+        unsigned n_side = 0;                      // layers finished so far (phase of the two service-warp barriers)
         for (int step = 0; step < a.n_steps; ++step) {
             if (a.forced_ids) tok = __ldg(a.forced_ids + step);
             if (tok < 0 || tok >= VOCAB) { if (tid == 0) atomicCAS(&ws->err, 0, (int)ERR_BAD_ARG); tok = 0; }
@@ -379,10 +524,11 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                 Q35_STAMP(0);
                 const unsigned ep = epoch_of(a, step, layer);
                 const bool dn = (L.type == 0);
+                bool att_owner = false;                    // attention layer: this CTA's chunk holds the current position
                 const bf16* w_post = (const bf16*)L.p[W_POST_NORM];
 
                 // ---- DeltaNet: issue the state / conv loads of stage B before any waiting ----
-                const int pp0 = part_begin(DN_V_SIZE / 2, b, G), pp1 = part_begin(DN_V_SIZE / 2, b + 1, G);   // value-row pairs
+                const int pp0 = s.pt[PT_PAIR0], pp1 = s.pt[PT_PAIR1];   // value-row pairs
                 float4 st0 = make_float4(0, 0, 0, 0), st1 = st0, cv0 = st0, cv1 = st0;
                 float* conv = a.conv_bufs + (size_t)i_dn * DN_CONV_CH * 4;
                 float* state = a.dn_states + (size_t)i_dn * DN_HEADS * DN_V * DN_K;
@@ -397,31 +543,31 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
 
                 // ================= stage A: input norm + fused projection =================
                 {
-                    uint32_t raw;
-                    if (layer == 0) raw = __ldg(reinterpret_cast<const uint32_t*>(a.embed + (size_t)tok * HIDDEN) + tid);
-                    else if (a.dbg_teacher) raw = __ldg(reinterpret_cast<const uint32_t*>(a.dbg_teacher + layer * HIDDEN) + tid);
-                    else raw = poll_word(&ws->h2[tid], epoch_of(a, step, layer - 1), ab);
-                    reinterpret_cast<uint32_t*>(s.h)[tid] = raw;
-                    rmsnorm_pair(raw, (const bf16*)L.p[W_IN_NORM], s.x, s.red);
+                    uint4 wn[4], xq[4];
+                    load_lane_chunks<FP4>((const bf16*)L.p[W_IN_NORM], wn);     // in flight while the input is awaited
+                    if (layer == 0) reinterpret_cast<uint32_t*>(s.h)[tid] = __ldg(reinterpret_cast<const uint32_t*>(a.embed + (size_t)tok * HIDDEN) + tid);
+                    else if (a.dbg_teacher) reinterpret_cast<uint32_t*>(s.h)[tid] = __ldg(reinterpret_cast<const uint32_t*>(a.dbg_teacher + layer * HIDDEN) + tid);
+                    else fetch_vec1024(ws->h2, epoch_of(a, step, layer - 1), s.h, ab);
                     cons_sync();
+                    norm_to_regs<FP4>(s.h, wn, xq);
                     Q35_STAMP(1);
-                    const int ntl = dn ? TILES_A_DN : TILES_A_FA;
-                    const int u0 = part_begin(ntl, b, G), u1 = part_begin(ntl, b + 1, G);
+                    const int u0 = s.pt[dn ? PT_A_DN0 : PT_A_FA0], u1 = s.pt[dn ? PT_A_DN1 : PT_A_FA1];
+                    bf16* stage_h = reinterpret_cast<bf16*>(s.stage);
                     if (FP4) {
                         // qkv / z (or q, k, v) tiles are NVFP4; the 16+16 rows of the b and a projections stay bf16
                         const int n_q = dn ? max(0, min(u1, (DN_CONV_CH + DN_V_SIZE) / 8) - u0) : (u1 - u0);
-                        consume_k1024_fp4<1>(ring, n_q, s.x, ab, [&](int row, const float (*acc)[2]) {
-                            s.stage[row >> 1] = pack_bf16x2(acc[0][0], acc[0][1]);
-                        });
-                        if (u1 - u0 > n_q)
-                            consume_k1024<1>(ring, u1 - u0 - n_q, s.x, ab, [&](int row, const float (*acc)[2]) {
-                                s.stage[(n_q * 8 + row) >> 1] = pack_bf16x2(acc[0][0], acc[0][1]);
-                            });
+                        consume_k1024_fp4<1>(ring, n_q, xq, ab, [&](int row, const float (&acc)[1]) { stage_h[row] = f2bf(acc[0]); });
+                        if (u1 - u0 > n_q) {
+                            // the few CTAs that own bf16 rows of this stage need the activations in the interleaved split too
+                            uint4 wi[4], xi[4];
+                            load_lane_chunks<false>((const bf16*)L.p[W_IN_NORM], wi);
+                            norm_to_regs<false>(s.h, wi, xi);
+                            consume_k1024<1>(ring, u1 - u0 - n_q, xi, ab, [&](int row, const float (&acc)[1]) { stage_h[n_q * 8 + row] = f2bf(acc[0]); });
+                        }
                     } else {
-                        consume_k1024<1>(ring, u1 - u0, s.x, ab, [&](int row, const float (*acc)[2]) {
-                            s.stage[row >> 1] = pack_bf16x2(acc[0][0], acc[0][1]);
-                        });
+                        consume_k1024<1>(ring, u1 - u0, xq, ab, [&](int row, const float (&acc)[1]) { stage_h[row] = f2bf(acc[0]); });
                     }
+                    Q35_STAMP(10);
                     // one coalesced store per CTA: a line that is written once reaches its pollers fastest
                     cons_sync();
                     if (tid < (u1 - u0) * 4) st_word(&ws->xa[u0 * 4 + tid], s.stage[tid], ep);
@@ -450,6 +596,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                         if (my_pair < pp1) vw_pre = poll_word(&ws->xa[(2 * DN_QK_SIZE + 2 * my_pair) >> 1], ep, ab);
                         const float wsum = warp_sum(sq);
                         cons_sync();
+                        Q35_STAMP(11);
                         if (lane == 0) s.red[warp] = wsum;
                         cons_sync();
                         if (act) {
@@ -501,37 +648,34 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                             ov[r] = warp_sum(o);
                             reinterpret_cast<float4*>(state + (size_t)(r0 + r) * DN_K)[lane] = t;
                         }
-                        if (lane == 0) s.stage[warp] = pack_bf16x2(ov[0], ov[1]);
+                        if (lane == 0) s.stage_b[warp] = pack_bf16x2(ov[0], ov[1]);
                     }
                     cons_sync();
-                    if (tid < pp1 - pp0) st_word(&ws->o[pp0 + tid], s.stage[tid], ep);
+                    if (tid < pp1 - pp0) st_word(&ws->o[pp0 + tid], s.stage_b[tid], ep);
 
                     Q35_STAMP(3);
-                    // ================= stage C (DeltaNet): gated norm (one head per warp), conv shift =================
+                    // ================= stage C (DeltaNet): gated norm (one head per warp) =================
                     {
                         const int h = warp;
-                        uint32_t o0, o1, z0, z1;
-                        {
-                            // z was published in stage A, long ago: its loads overlap the wait for `o`
-                            const u64* po = &ws->o[h * 64 + lane * 2];
-                            const u64* pz = &ws->xa[(DN_CONV_CH >> 1) + h * 64 + lane * 2];
-                            const u64 b0 = ld_word(pz), b1 = ld_word(pz + 1);
-                            poll2(po, po + 1, ep, ab, o0, o1);
-                            z0 = ((uint32_t)(b0 >> 32) == ep) ? (uint32_t)b0 : poll_word(pz, ep, ab);
-                            z1 = ((uint32_t)(b1 >> 32) == ep) ? (uint32_t)b1 : poll_word(pz + 1, ep, ab);
-                        }
+                        // z was published in stage A, long ago: everything that depends on z alone is done before `o` is awaited
+                        const u64* po = &ws->o[h * 64 + lane * 2];
+                        const u64* pz = &ws->xa[(DN_CONV_CH >> 1) + h * 64 + lane * 2];
                         const uint2 nrw = __ldg(reinterpret_cast<const uint2*>(L.p[W_GNORM]) + lane);
-                        const float ov[4] = {bf_lo(o0), bf_hi(o0), bf_lo(o1), bf_hi(o1)};
-                        const float zv[4] = {bf_lo(z0), bf_hi(z0), bf_lo(z1), bf_hi(z1)};
+                        uint32_t z0, z1, o0, o1;
+                        poll2(pz, pz + 1, ep, ab, z0, z1);
+                        const float sz[4] = {silu_f(bf_lo(z0)), silu_f(bf_hi(z0)), silu_f(bf_lo(z1)), silu_f(bf_hi(z1))};
                         const float nw[4] = {bf_lo(nrw.x), bf_hi(nrw.x), bf_lo(nrw.y), bf_hi(nrw.y)};
+                        poll2(po, po + 1, ep, ab, o0, o1);
+                        const float ov[4] = {bf_lo(o0), bf_hi(o0), bf_lo(o1), bf_hi(o1)};
                         const float var = warp_sum(ov[0] * ov[0] + ov[1] * ov[1] + ov[2] * ov[2] + ov[3] * ov[3]) * (1.0f / DN_V);
                         const float r = rsqrt_ieee(var + RMS_EPS);
+                        uint32_t out[2];
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const float n = rbf(ov[i] * r);
-                            const float t = rbf(nw[i] * n);
-                            s.x[h * DN_V + lane * 4 + i] = f2bf(t * silu_f(zv[i]));
+                        for (int i = 0; i < 2; ++i) {
+                            const float t0 = rbf(nw[2 * i] * rbf(ov[2 * i] * r)), t1 = rbf(nw[2 * i + 1] * rbf(ov[2 * i + 1] * r));
+                            out[i] = pack_bf16x2(t0 * sz[2 * i], t1 * sz[2 * i + 1]);
                         }
+                        *reinterpret_cast<uint2*>(s.x + h * DN_V + lane * 4) = make_uint2(out[0], out[1]);
                     }
                     ++i_dn;
                 } else {
@@ -539,13 +683,10 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                     // The context is split into chunks of >= 32 positions; CTA (kv head, chunk) owns one chunk.
                     bf16* kc = a.k_cache + (size_t)i_fa * FA_KV_HEADS * a.max_seq_len * FA_HEAD_DIM;
                     bf16* vc = a.v_cache + (size_t)i_fa * FA_KV_HEADS * a.max_seq_len * FA_HEAD_DIM;
-                    const int Lc = pos + 1;
-                    int nchunk = (Lc + 31) / 32;
-                    { const int cap = min(ATT_MAX_CHUNKS, G / FA_KV_HEADS); if (nchunk > cap) nchunk = cap; }
-                    const int clen = (Lc + nchunk - 1) / nchunk;            // <= ATT_CHUNK_MAX by the host-side limit on max_seq_len
-                    const bool att_cta = b < FA_KV_HEADS * nchunk;
-                    const int kvh = b / nchunk, chunk = b % nchunk;
-                    const int j0 = chunk * clen, j1 = min(Lc, j0 + clen);
+                    const AttGeom ag = att_geom(pos, b, G);
+                    const int nchunk = ag.nchunk, kvh = ag.kvh, chunk = ag.chunk, j0 = ag.j0, j1 = ag.j1;
+                    const bool att_cta = ag.att_cta;
+                    att_owner = ag.owns_pos;
                     if (att_cta) {
                         if (warp < FA_GQA + 1) {
                             // warps 0..3: the four query heads of this kv head; warp 4: the new key.
@@ -585,21 +726,16 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                             float* dst = isq ? s.q[warp] : s.kcur;
 #pragma unroll
                             for (int i = 0; i < 4; ++i) { dst[2 * lane + 64 * i] = xv[2 * i]; dst[2 * lane + 64 * i + 1] = xv[2 * i + 1]; }
-                            if (!isq && pos >= j0 && pos < j1) {
-                                uint32_t* krow = reinterpret_cast<uint32_t*>(kc + ((size_t)kvh * a.max_seq_len + pos) * FA_HEAD_DIM);
-#pragma unroll
-                                for (int i = 0; i < 4; ++i) krow[lane + 32 * i] = pack_bf16x2(xv[2 * i], xv[2 * i + 1]);
-                                __threadfence();
-                            }
-                        } else if (warp == FA_GQA + 1 && pos >= j0 && pos < j1) {
-                            uint32_t* vrow = reinterpret_cast<uint32_t*>(vc + ((size_t)kvh * a.max_seq_len + pos) * FA_HEAD_DIM);
+                        } else if (warp == FA_GQA + 1 && ag.owns_pos) {
+                            // the new value row stays in shared memory for this token; the service warp appends it (and the
+                            // key row from kcur) to the cache
                             uint32_t wv[4];
                             poll4(&ws->xa[((FA_QPROJ + FA_KV_SIZE + kvh * FA_HEAD_DIM) >> 1) + lane], 32, ep, ab, wv);
 #pragma unroll
-                            for (int i = 0; i < 4; ++i) vrow[lane + 32 * i] = wv[i];
-                            __threadfence();
+                            for (int i = 0; i < 4; ++i) s.vcur[lane + 32 * i] = wv[i];
                         }
                         cons_sync();
+                        if (ag.owns_pos && tid == 0) { mbar_arrive(smem_u32(&s.side_go), 1); }
                         // ---- scores of this chunk, two positions per warp in flight ----
                         {
                             float qr[FA_GQA][8];
@@ -680,7 +816,8 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                             for (int jj = 0; jj < cn; jj += 32) {
                                 uint32_t vr[32];
 #pragma unroll
-                                for (int u = 0; u < 32; ++u) vr[u] = (jj + u < cn) ? ld_cg(vb + (size_t)(jj + u) * (FA_HEAD_DIM / 2)) : 0u;
+                                for (int u = 0; u < 32; ++u)
+                                    vr[u] = (jj + u >= cn) ? 0u : (j0 + jj + u == pos) ? s.vcur[d2] : ld_cg(vb + (size_t)(jj + u) * (FA_HEAD_DIM / 2));
 #pragma unroll
                                 for (int u = 0; u < 32; ++u) {
                                     const float p = (jj + u < cn) ? s.p[g][jj + u] : 0.f;
@@ -688,53 +825,41 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                                     acc1 = fmaf(p, bf_hi(vr[u]), acc1);
                                 }
                             }
-                            reinterpret_cast<float2*>(ws->att_part[chunk][kvh * FA_GQA + g])[d2] = make_float2(acc0, acc1);
+                            // the partial travels as flagged words like every other hand-off: no fence, no separate flag
+                            st_word(&ws->att_part[chunk][kvh * FA_GQA + g][2 * d2], __float_as_uint(acc0), ep);
+                            st_word(&ws->att_part[chunk][kvh * FA_GQA + g][2 * d2 + 1], __float_as_uint(acc1), ep);
                         }
-                        __threadfence();
-                        cons_sync();
-                        if (tid == 0) st_release(&ws->att_flag[kvh][chunk], ep);
                     }
                     // ---- B3: CTA h < 8 merges the partials of query head h and applies the sigmoid gate ----
                     if (b < FA_Q_HEADS) {
                         const int qh = b;
-                        if (tid < nchunk) {
-                            unsigned it = 0;
-                            while (ld_acquire(&ws->att_flag[qh / FA_GQA][tid]) != ep && !ab.on()) {
-                                if (++it > POLL_LIMIT) { ab.raise(ERR_BARRIER_TIMEOUT); break; }
-                            }
-                        }
-                        cons_sync();
+                        cons_sync();                      // P of this CTA's chunk (s.p) is no longer needed: it holds the group sums now
                         {
-                            // 8 groups of 64 threads: group q sums chunks q, q+8, ... (all its loads in flight at once: one L2
-                            // round trip), then thread t < 64 adds the 8 group sums in group order and applies the gate
-                            const int d = (tid & 63) * 4, grp = tid >> 6;
-                            float4 pv[ATT_MAX_CHUNKS / 8];
+                            // 4 groups of 128 threads: group q sums chunks q, q+4, ... in ascending order, two dims per thread,
+                            // four chunks (8 flagged words) in flight per round trip
+                            const int d = tid & 127, grp = tid >> 7;
+                            float a0 = 0.f, a1 = 0.f;
+                            for (int c0 = grp; c0 < nchunk; c0 += 16) {
+                                uint32_t w[8];
+                                poll_pairs<4>(&ws->att_part[c0][qh][2 * d], 4 * FA_Q_HEADS * FA_HEAD_DIM, (nchunk - c0 + 3) / 4, ep, ab, w);
 #pragma unroll
-                            for (int u = 0; u < ATT_MAX_CHUNKS / 8; ++u) {
-                                const int c = grp + 8 * u;
-                                pv[u] = (c < nchunk) ? ld_cg(reinterpret_cast<const float4*>(&ws->att_part[c][qh][d])) : make_float4(0.f, 0.f, 0.f, 0.f);
+                                for (int u = 0; u < 4; ++u) { a0 += __uint_as_float(w[2 * u]); a1 += __uint_as_float(w[2 * u + 1]); }
                             }
-                            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                            for (int u = 0; u < ATT_MAX_CHUNKS / 8; ++u) { acc.x += pv[u].x; acc.y += pv[u].y; acc.z += pv[u].z; acc.w += pv[u].w; }
-                            reinterpret_cast<float4*>(&s.p[0][0])[tid] = acc;         // P of this CTA's chunk is no longer needed: [8 groups][64 x float4]
+                            reinterpret_cast<float2*>(&s.p[0][0])[grp * 128 + d] = make_float2(a0, a1);
                         }
                         cons_sync();
-                        if (tid < 64) {
-                            const int d = tid * 4;
-                            uint32_t g0, g1;
+                        if (tid < 128) {
+                            const int d = 2 * tid;
                             const int ge = qh * 2 * FA_HEAD_DIM + FA_HEAD_DIM + d;
-                            poll2(&ws->xa[ge >> 1], &ws->xa[(ge >> 1) + 1], ep, ab, g0, g1);
-                            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                            const uint32_t gw = poll_word(&ws->xa[ge >> 1], ep, ab);
+                            float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-                            for (int q = 0; q < 8; ++q) {
-                                const float4 v = reinterpret_cast<const float4*>(&s.p[0][0])[q * 64 + tid];
-                                acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+                            for (int q = 0; q < 4; ++q) {
+                                const float2 v = reinterpret_cast<const float2*>(&s.p[0][0])[q * 128 + tid];
+                                acc.x += v.x; acc.y += v.y;
                             }
-                            const float u0 = rbf(acc.x) * rbf(sigmoid_f(bf_lo(g0))), u1 = rbf(acc.y) * rbf(sigmoid_f(bf_hi(g0)));
-                            const float u2 = rbf(acc.z) * rbf(sigmoid_f(bf_lo(g1))), u3 = rbf(acc.w) * rbf(sigmoid_f(bf_hi(g1)));
+                            const float u0 = rbf(acc.x) * rbf(sigmoid_f(bf_lo(gw))), u1 = rbf(acc.y) * rbf(sigmoid_f(bf_hi(gw)));
                             st_word(&ws->o[(qh * FA_HEAD_DIM + d) >> 1], pack_bf16x2(u0, u1), ep);
-                            st_word(&ws->o[((qh * FA_HEAD_DIM + d) >> 1) + 1], pack_bf16x2(u2, u3), ep);
                         }
                     }
                     Q35_STAMP(3);
@@ -748,11 +873,14 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                     ++i_fa;
                 }
                 cons_sync();
+                // DeltaNet: every warp has its head's `o`, so all CTAs are past stage B.  Attention: the CTA that holds the new
+                // K / V row has signalled already, the others have no side work.
+                if (tid == 0 && (dn || !att_owner)) mbar_arrive(smem_u32(&s.side_go), 1);
                 Q35_STAMP(4);
                 // ---- stage C tail: output projection (K = 2048, 4 rows per tile) + residual ----
                 {
                     const bf16* hin = s.h;
-                    const int u0 = part_begin(TILES_C, b, G), nt = part_begin(TILES_C, b + 1, G) - u0;
+                    const int u0 = s.pt[PT_C0], nt = s.pt[PT_C1] - u0;
                     if (FP4) {
                         // 4 rows x 1024 bytes of nibbles per tile; warps 0-7: row w/2, K half w%2 (32 groups of 32, one per lane)
                         float x[32];
@@ -773,62 +901,62 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                             }
                         }
                     } else {
-                    float x[16];
-                    unpack8(*reinterpret_cast<const uint4*>(s.x + (warp & 3) * 512 + lane * 8), x);
-                    unpack8(*reinterpret_cast<const uint4*>(s.x + (warp & 3) * 512 + (32 + lane) * 8), x + 8);
-                    for (int ti = 0; ti < nt; ++ti) {
-                        const unsigned tile = ring.t + (unsigned)ti;
-                        mbar_wait(ring.full_bar(tile), ring.phase(tile), ab);
-                        const uint32_t base = ring.slot_addr(tile) + (uint32_t)(warp >> 2) * 4096u + (uint32_t)(warp & 3) * 1024u + (uint32_t)lane * 16u;
-                        const uint4 q0 = lds128(base), q1 = lds128(base + 512);
-                        const float acc = warp_sum(dot8(q1, x + 8, dot8(q0, x, 0.f)));
-                        if (lane == 0) { s.part[ti * 16 + warp] = acc; mbar_arrive(ring.empty_bar(tile), 1); }
+                    // two tiles at a time: warp = (tile w/8, row (w/2)%4, K half w%2), so a CTA with two tiles (most have one
+                    // or two) is done as soon as a CTA with one
+                    const int crow = (warp >> 1) & 3, chalf = warp & 1;
+                    uint4 xc[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) xc[j] = *reinterpret_cast<const uint4*>(s.x + chalf * 1024 + (j * 32 + lane) * 8);
+                    for (int tb = 0; tb < nt; tb += 2) {
+                        const int ti = tb + (warp >> 3);
+                        if (ti < nt) {
+                            const unsigned tile = ring.t + (unsigned)ti;
+                            mbar_wait(ring.full_bar(tile), ring.phase(tile), ab);
+                            const uint32_t base = ring.slot_addr(tile) + (uint32_t)crow * 4096u + (uint32_t)chalf * 2048u + (uint32_t)lane * 16u;
+                            uint4 wq[4];
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) wq[j] = lds128(base + j * 512);
+                            const float a0 = dot8m(wq[2], xc[2], dot8m(wq[0], xc[0], 0.f)), a1 = dot8m(wq[3], xc[3], dot8m(wq[1], xc[1], 0.f));
+                            const float acc = warp_sum(a0 + a1);
+                            if (lane == 0) { s.part[ti * 16 + crow * 2 + chalf] = acc; mbar_arrive(ring.empty_bar(tile), 2); }
+                        }
                     }
                     }
                     ring.t += (unsigned)nt;
                     cons_sync();
                     if (tid < nt * 2) {
                         const int ti = tid >> 1, pr = tid & 1;
-                        const float* pp = &s.part[ti * 16 + pr * 8];
-                        const float y0 = ((pp[0] + pp[1]) + pp[2]) + pp[3], y1 = ((pp[4] + pp[5]) + pp[6]) + pp[7];
+                        // partial sums of rows 2 pr and 2 pr + 1: NVFP4 keeps four slots per row, bf16 one per K half
+                        const float* pp = &s.part[ti * 16 + pr * (FP4 ? 8 : 4)];
+                        const float y0 = FP4 ? ((pp[0] + pp[1]) + pp[2]) + pp[3] : pp[0] + pp[1];
+                        const float y1 = FP4 ? ((pp[4] + pp[5]) + pp[6]) + pp[7] : pp[2] + pp[3];
                         const int row = (u0 + ti) * 4 + 2 * pr;
                         st_word(&ws->h1[row >> 1], pack_bf16x2(bf2f(hin[row]) + rbf(y0), bf2f(hin[row + 1]) + rbf(y1)), ep);
                     }
                 }
 
                 Q35_STAMP_ALL(5);
-                if (dn) {
-                    // Conv-window shift, off the critical path.  This CTA has seen all of `o`, so every CTA
-                    // finished stage B and nobody reads this layer's old window any more.  The fence orders the
-                    // new window before this CTA's next publication (stage D), which the next token's readers follow.
-                    for (int c = part_begin(DN_CONV_CH / 2, b, G) + tid; c < part_begin(DN_CONV_CH / 2, b + 1, G); c += NCONS) {
-                        const uint32_t xw = poll_word(&ws->xa[c], ep, ab);
-                        const float4 c0 = ld_cg(reinterpret_cast<const float4*>(conv) + 2 * c);
-                        const float4 c1 = ld_cg(reinterpret_cast<const float4*>(conv) + 2 * c + 1);
-                        reinterpret_cast<float4*>(conv)[2 * c] = make_float4(c0.y, c0.z, c0.w, bf_lo(xw));
-                        reinterpret_cast<float4*>(conv)[2 * c + 1] = make_float4(c1.y, c1.z, c1.w, bf_hi(xw));
-                        __threadfence();
-                    }
-                }
                 // ================= stage D: post norm, gate/up with SiLU*up =================
                 {
-                    const uint32_t raw = poll_word(&ws->h1[tid], ep, ab);
-                    reinterpret_cast<uint32_t*>(s.h1)[tid] = raw;
-                    rmsnorm_pair(raw, w_post, s.x, s.red);
+                    uint4 wn[4], xq[4];
+                    load_lane_chunks<FP4>(w_post, wn);
+                    fetch_vec1024(ws->h1, ep, s.h1, ab);
                     cons_sync();
+                    norm_to_regs<FP4>(s.h1, wn, xq);
                     Q35_STAMP(6);
-                    const int u0 = part_begin(UNITS_D, b, G), u1 = part_begin(UNITS_D, b + 1, G);
-                    auto epi_d = [&](int row, const float (*acc)[2]) {
-                        const float m0 = rbf(silu_f(rbf(acc[0][0]))) * rbf(acc[1][0]);
-                        const float m1 = rbf(silu_f(rbf(acc[0][1]))) * rbf(acc[1][1]);
-                        s.stage[row >> 1] = pack_bf16x2(m0, m1);
+                    const int u0 = s.pt[PT_D0], u1 = s.pt[PT_D1];
+                    bf16* stage_h = reinterpret_cast<bf16*>(s.stage);
+                    auto epi_d = [&](int row, const float (&acc)[2]) {
+                        stage_h[row] = f2bf(rbf(silu_f(rbf(acc[0]))) * rbf(acc[1]));
                     };
-                    if (FP4) consume_k1024_fp4<2>(ring, u1 - u0, s.x, ab, epi_d);
-                    else consume_k1024<2>(ring, u1 - u0, s.x, ab, epi_d);
+                    if (FP4) {
+                        consume_k1024_fp4<2>(ring, u1 - u0, xq, ab, epi_d);
+                    } else {
+                        consume_k1024<2>(ring, u1 - u0, xq, ab, epi_d);
+                    }
                     cons_sync();
                     if (tid < (u1 - u0) * 4) st_word(&ws->m[u0 * 4 + tid], s.stage[tid], ep);
                 }
-
                 Q35_STAMP_ALL(7);
                 // ================= stage E: down projection (K = 3584, 2 rows per tile) + residual =================
                 {
@@ -842,7 +970,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                     }
                     cons_sync();
                     Q35_STAMP(8);
-                    const int u0 = part_begin(TILES_E, b, G), nt = part_begin(TILES_E, b + 1, G) - u0;
+                    const int u0 = s.pt[PT_E0], nt = s.pt[PT_E1] - u0;
                     if (FP4) {
                         // 2 rows x 1792 bytes of nibbles per tile; warp: tile w/4, row (w%4)/2, K half w%2 = 56 groups of 32:
                         // lane l takes group l and, for l < 24, group 32 + l
@@ -876,15 +1004,21 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                             const unsigned tile = ring.t + (unsigned)ti;
                             mbar_wait(ring.full_bar(tile), ring.phase(tile), ab);
                             const uint32_t base = ring.slot_addr(tile) + (uint32_t)((warp & 3) >> 1) * 7168u + (uint32_t)(warp & 1) * 3584u + (uint32_t)lane * 16u;
-                            float acc = 0.f;
+                            uint4 wq[7];
 #pragma unroll
-                            for (int j = 0; j < 7; ++j) acc = dot8p(lds128(base + j * 512), xp[j], acc);
-                            acc = warp_sum(acc);
+                            for (int j = 0; j < 7; ++j) wq[j] = lds128(base + j * 512);
+                            float a0 = dot8m(wq[0], xp[0], 0.f), a1 = dot8m(wq[1], xp[1], 0.f), a2 = dot8m(wq[2], xp[2], 0.f);
+                            a0 = dot8m(wq[3], xp[3], a0); a1 = dot8m(wq[4], xp[4], a1); a2 = dot8m(wq[5], xp[5], a2);
+                            a0 = dot8m(wq[6], xp[6], a0);
+                            const float acc = warp_sum((a0 + a1) + a2);
                             if (lane == 0) { s.part[ti * 4 + (warp & 3)] = acc; mbar_arrive(ring.empty_bar(tile), 4); }
                         }
                     }
                     }
                     ring.t += (unsigned)nt;
+                    // the layer's output is the publication that the next token's readers of the conv window follow
+                    if (tid == 0) mbar_wait(smem_u32(&s.side_done), n_side & 1u, ab);
+                    ++n_side;
                     cons_sync();
                     if (tid < nt) {
                         const float y0 = s.part[tid * 4] + s.part[tid * 4 + 1], y1 = s.part[tid * 4 + 2] + s.part[tid * 4 + 3];
@@ -903,20 +1037,23 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                 const unsigned ep_lm = epoch_of(a, step, 24);
                 const int stamp_row = 24;
                 Q35_STAMP(0);
-                const uint32_t raw = poll_word(&ws->h2[tid], epoch_of(a, step, n_layers - 1), ab);
+                uint4 wn[4], xq[4];
+                load_lane_chunks<FP4>(a.final_norm, wn);
+                fetch_vec1024(ws->h2, epoch_of(a, step, n_layers - 1), s.h, ab);
                 Q35_STAMP(1);
-                rmsnorm_pair(raw, a.final_norm, s.x, s.red);
                 cons_sync();
+                norm_to_regs<FP4>(s.h, wn, xq);
                 float best = -INFINITY;
                 int best_i = 0x7fffffff;
                 float* lg = (last_step ? a.logits_out : nullptr);
                 // rows of the vocabulary owned by this CTA: [lm_row0, ...), in 8-row tiles (bf16) or 128-row blocks (NVFP4)
-                const int lm_row0 = FP4 ? part_begin(FP4_LM_BLOCKS, b, G) * 128 : part_begin(TILES_LM, b, G) * 8;
+                const int lm_row0 = FP4 ? s.pt[PT_LMB0] * 128 : s.pt[PT_LM0] * 8;
                 if (FP4) {
                     // tensor-core layout: one E4M3 scale per 16 weights, stored in 512-byte tiles of 128 rows x 4 blocks
                     float x[32];
-                    load_x32(s.x, 32 * lane, x);
-                    const int B0 = part_begin(FP4_LM_BLOCKS, b, G), B1 = part_begin(FP4_LM_BLOCKS, b + 1, G);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) unpack8(xq[j], x + 8 * j);
+                    const int B0 = s.pt[PT_LMB0], B1 = s.pt[PT_LMB1];
                     for (int blk = B0; blk < B1; ++blk) {
                         const unsigned tile_s = ring.t, tile_p = ring.t + 1u + (unsigned)(warp >> 2);
                         mbar_wait(ring.full_bar(tile_s), ring.phase(tile_s), ab);
@@ -945,17 +1082,20 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                         ring.t += 5u;
                     }
                 } else {
-                    const int u0 = part_begin(TILES_LM, b, G), u1 = part_begin(TILES_LM, b + 1, G);
-                    consume_k1024<1>(ring, u1 - u0, s.x, ab, [&](int row, const float (*acc)[2]) {
+                    const int u0 = s.pt[PT_LM0], u1 = s.pt[PT_LM1];
+                    // lane 0 sees the even rows of its warp's share, lane 16 the odd ones, each in ascending order
+                    consume_k1024<1>(ring, u1 - u0, xq, ab, [&](int row, const float (&acc)[1]) {
                         const int r0 = u0 * 8 + row;
-                        const float v0 = rbf(acc[0][0]), v1 = rbf(acc[0][1]);
-                        if (lg) { lg[r0] = v0; lg[r0 + 1] = v1; }
+                        const float v0 = rbf(acc[0]);
+                        if (lg) lg[r0] = v0;
                         if (v0 > best) { best = v0; best_i = r0; }
-                        if (v1 > best) { best = v1; best_i = r0 + 1; }
                     });
+                    const float ob = __shfl_sync(0xffffffffu, best, 16);
+                    const int oi = __shfl_sync(0xffffffffu, best_i, 16);
+                    if (ob > best || (ob == best && oi < best_i)) { best = ob; best_i = oi; }
                 }
                 Q35_STAMP(2);
-                // lane 0 of every warp holds that warp's best (rows ascend within a warp)
+                // lane 0 of every warp holds that warp's best
                 cons_sync();
                 if (lane == 0) { s.part[warp] = best; reinterpret_cast<int*>(s.part)[NCONS_WARPS + warp] = best_i; }
                 cons_sync();
@@ -980,7 +1120,7 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                         if (c < G) {
                             const uint32_t w = ((uint32_t)(v[k] >> 32) == ep_lm) ? (uint32_t)v[k] : poll_word(&ws->lm[0][c], ep_lm, ab);
                             const float val = __uint_as_float(w & 0xffff0000u);
-                            const int idx = (FP4 ? part_begin(FP4_LM_BLOCKS, c, G) * 128 : part_begin(TILES_LM, c, G) * 8) + (int)(w & 0xffffu);
+                            const int idx = s.lm_row0[c] + (int)(w & 0xffffu);
                             if (val > bv || (val == bv && idx < bi)) { bv = val; bi = idx; }
                         }
                     }

@@ -23,7 +23,8 @@ constexpr int ATT_CHUNK_MAX = 512;      // longest chunk: MAX_CTX / ATT_MAX_CHUN
 
 constexpr int NCONS_WARPS = 16;
 constexpr int NCONS = NCONS_WARPS * 32;             // 512 consumer threads
-constexpr int STREAM_THREADS = NCONS + 32;          // + one producer warp
+// + one producer warp (weight stream) + one service warp (cache / conv-window updates and their fences, off the consumers' path)
+constexpr int STREAM_THREADS = NCONS + 64;
 constexpr int SLOT_BYTES = 16384;
 constexpr int NSLOTS = 12;
 
@@ -45,8 +46,7 @@ struct StreamWorkspace {
     alignas(256) u64 m[INTER / 2];                  // silu(gate) * up
     alignas(256) u64 h2[HIDDEN / 2];                // layer output
     alignas(256) u64 lm[2][1024];                   // per CTA: {bf16 max bits, epoch}, {arg-max, epoch}
-    alignas(256) unsigned att_flag[FA_KV_HEADS][ATT_MAX_CHUNKS];
-    alignas(256) float att_part[ATT_MAX_CHUNKS][FA_Q_HEADS][FA_HEAD_DIM];
+    alignas(256) u64 att_part[ATT_MAX_CHUNKS][FA_Q_HEADS][FA_HEAD_DIM];   // per chunk: f32 partial of P.V, one flagged word per value
     alignas(256) u64 att_stat[FA_Q_HEADS][ATT_MAX_CHUNKS][2];   // per head and chunk: {max, epoch}, {sum exp, epoch}
 };
 
@@ -186,6 +186,27 @@ __device__ __forceinline__ void poll_n(const u64* p, int stride, int n, uint32_t
     for (int i = 0; i < N; ++i) o[i] = (uint32_t)v[i];
 }
 
+// N units of two adjacent words, the units `stride` words apart (only the first `n` units are live): o[2 i], o[2 i + 1].
+template <int N>
+__device__ __forceinline__ void poll_pairs(const u64* p, int stride, int n, uint32_t epoch, const Abort& ab, uint32_t (&o)[2 * N]) {
+    u64 v[2 * N];
+    unsigned pending = 0;
+#pragma unroll
+    for (int i = 0; i < 2 * N; ++i) if ((i >> 1) < n) v[i] = ld_word(p + (i >> 1) * stride + (i & 1));
+#pragma unroll
+    for (int i = 0; i < 2 * N; ++i) if ((i >> 1) < n && (uint32_t)(v[i] >> 32) != epoch) pending |= 1u << i;
+    unsigned it = 0;
+    while (pending && !ab.on()) {
+#pragma unroll
+        for (int i = 0; i < 2 * N; ++i) if (pending & (1u << i)) v[i] = ld_word(p + (i >> 1) * stride + (i & 1));
+#pragma unroll
+        for (int i = 0; i < 2 * N; ++i) if ((pending & (1u << i)) && (uint32_t)(v[i] >> 32) == epoch) pending &= ~(1u << i);
+        if (++it > POLL_LIMIT || ((it & 4095u) == 0 && ld_volatile(ab.g_err) != 0)) { ab.raise(ERR_BARRIER_TIMEOUT); break; }
+    }
+#pragma unroll
+    for (int i = 0; i < 2 * N; ++i) o[i] = ((i >> 1) < n) ? (uint32_t)v[i] : 0u;
+}
+
 __device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t parity, const Abort& ab) {
     unsigned it = 0;
     while (!mbar_try_wait(bar, parity)) {
@@ -235,6 +256,37 @@ __device__ __forceinline__ float dot8p(const uint4 q, const uint4 y, float a) {
     a = fmaf(bf_lo(q.w), bf_lo(y.w), a); a = fmaf(bf_hi(q.w), bf_hi(y.w), a);
     return a;
 }
+// d = a_lo * b_lo + a_hi * b_hi + d for two packed bf16 pairs, f32 accumulate: the mixed-precision FMA of sm_100
+// (fma.rn.f32.bf16) takes its bf16 operands as they are, so no conversion instruction precedes it.  A product of two
+// bf16 values is exact in f32, hence each step rounds once, exactly like fmaf on the widened values.
+__device__ __forceinline__ float fma2_bf16(uint32_t a, uint32_t b, float d) {
+    asm("{\n\t.reg .b16 al, ah, bl, bh;\n\t"
+        "mov.b32 {al, ah}, %1;\n\t"
+        "mov.b32 {bl, bh}, %2;\n\t"
+        "fma.rn.f32.bf16 %0, al, bl, %0;\n\t"
+        "fma.rn.f32.bf16 %0, ah, bh, %0;\n\t}"
+        : "+f"(d) : "r"(a), "r"(b));
+    return d;
+}
+// 8 bf16 weights (one 16-byte chunk) times 8 bf16 activations (packed the same way)
+__device__ __forceinline__ float dot8m(const uint4 w, const uint4 y, float a) {
+    a = fma2_bf16(w.x, y.x, a);
+    a = fma2_bf16(w.y, y.y, a);
+    a = fma2_bf16(w.z, y.z, a);
+    return fma2_bf16(w.w, y.w, a);
+}
+// Sums two per-lane values over the warp with five shuffles instead of ten: after the first exchange lanes 0-15 carry
+// `a`, lanes 16-31 carry `b`; on return every lane below 16 holds the total of a, every lane from 16 up the total of b.
+__device__ __forceinline__ float warp_sum2(float a, float b) {
+    const bool hi = (threadIdx.x & 16) != 0;
+    float keep = hi ? b : a;
+    const float send = hi ? a : b;
+    keep += __shfl_xor_sync(0xffffffffu, send, 16);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) keep += __shfl_xor_sync(0xffffffffu, keep, o);
+    return keep;
+}
+
 __device__ __forceinline__ void unpack8(const uint4 v, float* x) {
     x[0] = bf_lo(v.x); x[1] = bf_hi(v.x); x[2] = bf_lo(v.y); x[3] = bf_hi(v.y);
     x[4] = bf_lo(v.z); x[5] = bf_hi(v.z); x[6] = bf_lo(v.w); x[7] = bf_hi(v.w);

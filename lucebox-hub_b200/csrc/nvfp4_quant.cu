@@ -5,8 +5,14 @@
 //   * tensor-core layout   quantize_nvfp4_lm_kernel, kernel_gb10_nvfp4.cu:1366-1430, launcher :1878-1892
 //     16-element blocks, UE4M3 scale = sat_rn(max(amax/6, 2^-28)), elements divided by the decoded scale and
 //     rounded to E2M1 with round-to-nearest-even, scale bytes in 128-row x 4-column tiles of 512 bytes.
-// Pure streaming kernels: one 16-byte (or 2 x 16-byte) load per thread, coalesced along K.  IEEE f32
-// arithmetic (no fast-math), so the bytes equal oracle/nvfp4_ref.py exactly.
+// Pure streaming kernels: one 16-byte (or 2 x 16-byte) load per thread, coalesced along K.
+// The packed bytes must equal those of the reference's own kernels, and the reference builds with --use_fast_math
+// (models/qwen35_0p8b/setup.py): its `amax / 6.0f`, `1.0f / scale` and `1.0f / decoded_scale` are approximate divisions
+// and reciprocals.  This file is therefore compiled with --use_fast_math too (build.py) and writes those three
+// expressions in the reference's form, so the compiler lowers them the same way; everything else in it is exact
+// either way (comparisons, products of two floats, conversions).  tests/test_nvfp4_gpu.py compares the bytes with the
+// reference's kernels compiled from its own source; the IEEE restatement in oracle/nvfp4_ref.py differs from both in the
+// rare element that sits on a rounding boundary of the approximate reciprocal.
 #include <cuda_fp16.h>
 #include <cuda_fp4.h>
 #include <cuda_fp8.h>
@@ -37,17 +43,17 @@ __global__ void __launch_bounds__(256) quantize_nvfp4_kernel(const bf16* __restr
             amax = fmaxf(amax, fmaxf(fmaxf(fabsf(bf_lo(v.x)), fabsf(bf_hi(v.x))), fmaxf(fabsf(bf_lo(v.y)), fabsf(bf_hi(v.y)))));
             amax = fmaxf(amax, fmaxf(fmaxf(fabsf(bf_lo(v.z)), fabsf(bf_hi(v.z))), fmaxf(fabsf(bf_lo(v.w)), fabsf(bf_hi(v.w)))));
         }
-        const float scale = (amax > 0.f) ? __fdiv_rn(amax, 6.0f) : 1.0f;
-        scales[gid] = __float2half_rn(scale);
-        const float inv = __fdiv_rn(1.0f, scale);
+        const float scale = (amax > 0.0f) ? (amax / 6.0f) : 1.0f;          // kernel_gb10_nvfp4.cu:1791
+        scales[gid] = __float2half(scale);
+        const float inv = 1.0f / scale;                                    // :1801
         for (int i = 0; i < group_size / 8; ++i) {
             const uint4 v = __ldg(src + i);
             const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
             uint32_t out = 0;
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                const unsigned lo = (amax > 0.f) ? fp4_threshold_code(__fmul_rn(bf_lo(wd[k]), inv)) : 0u;
-                const unsigned hi = (amax > 0.f) ? fp4_threshold_code(__fmul_rn(bf_hi(wd[k]), inv)) : 0u;
+                const unsigned lo = (amax > 0.f) ? fp4_threshold_code(bf_lo(wd[k]) * inv) : 0u;
+                const unsigned hi = (amax > 0.f) ? fp4_threshold_code(bf_hi(wd[k]) * inv) : 0u;
                 out |= (lo | (hi << 4)) << (8 * k);
             }
             reinterpret_cast<uint32_t*>(dst)[i] = out;
@@ -68,15 +74,15 @@ __global__ void __launch_bounds__(256) quantize_nvfp4_lm_kernel(const bf16* __re
         float amax = 0.f;
 #pragma unroll
         for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fmaxf(fabsf(bf_lo(wd[k])), fabsf(bf_hi(wd[k]))));
-        const float scale_f = fmaxf(__fmul_rn(amax, 1.0f / 6.0f), 1.0f / (float)(1 << 28));
+        const float scale_f = fmaxf(amax * (1.0f / 6.0f), 1.0f / float(1 << 28));   // kernel_gb10_nvfp4.cu:1402
         const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(scale_f, __NV_SATFINITE, __NV_E4M3);
         const __half_raw hr = __nv_cvt_fp8_to_halfraw(s8, __NV_E4M3);
         const float dec = __half2float(*reinterpret_cast<const __half*>(&hr));
-        const float inv = (dec > 0.f) ? __fdiv_rn(1.0f, dec) : 0.f;
+        const float inv = (dec > 0.0f) ? (1.0f / dec) : 0.0f;                       // :1406
         unsigned long long out = 0;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-            const float2 f2 = make_float2(__fmul_rn(bf_lo(wd[k]), inv), __fmul_rn(bf_hi(wd[k]), inv));
+            const float2 f2 = make_float2(bf_lo(wd[k]) * inv, bf_hi(wd[k]) * inv);
             const __nv_fp4x2_storage_t p = __nv_cvt_float2_to_fp4x2(f2, __NV_E2M1, cudaRoundNearest);
             out |= (unsigned long long)(uint8_t)p << (8 * k);
         }

@@ -139,9 +139,53 @@ static __global__ void pf_conv_state_kernel(const bf16* __restrict__ proj, int l
     reinterpret_cast<float4*>(conv)[ch] = st;
 }
 
-// ---- chunk-local part of the gated delta rule: one CTA (256 threads) per (chunk, head) --------------
+// ---- TF32 tensor-core helpers (legacy mma.sync path, m16n8k8) --------------------------------------------------------
+// The chunk kernels multiply f32 matrices whose results feed a recurrent f32 state, so plain TF32 (10 mantissa bits) is
+// not enough.  Each operand is split x = hi + lo with hi = tf32(x), lo = tf32(x - hi), and a product is taken as
+// a_lo b_hi + a_hi b_lo + a_hi b_hi with f32 accumulation ("3xTF32"): about 21 bits per operand, f32 sums.
+// Fragment layout of mma.m16n8k8 (g = lane / 4, t = lane % 4):  A (16x8, row):  a0 (g, t)  a1 (g+8, t)  a2 (g, t+4)  a3 (g+8, t+4);
+// B (8x8, k x n):  b0 (t, g)  b1 (t+4, g);   C (16x8):  c0 (g, 2t)  c1 (g, 2t+1)  c2 (g+8, 2t)  c3 (g+8, 2t+1).
+__device__ __forceinline__ uint32_t tf32_of(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+__device__ __forceinline__ void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
+    hi = tf32_of(x);
+    lo = tf32_of(x - __uint_as_float(hi));
+}
+__device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_3xtf32(float (&c)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4], uint32_t bh0, uint32_t bh1,
+                                           uint32_t bl0, uint32_t bl1) {
+    mma_tf32(c, al, bh0, bh1);
+    mma_tf32(c, ah, bl0, bl1);
+    mma_tf32(c, ah, bh0, bh1);
+}
+// A fragment of a row-major f32 matrix in shared memory (rows m0.., columns k0..), split into hi / lo
+__device__ __forceinline__ void load_a_split(const float* A, int ld, int m0, int k0, uint32_t (&ah)[4], uint32_t (&al)[4]) {
+    const int g = (threadIdx.x & 31) >> 2, t = threadIdx.x & 3;
+    tf32_split(A[(m0 + g) * ld + k0 + t], ah[0], al[0]);
+    tf32_split(A[(m0 + g + 8) * ld + k0 + t], ah[1], al[1]);
+    tf32_split(A[(m0 + g) * ld + k0 + t + 4], ah[2], al[2]);
+    tf32_split(A[(m0 + g + 8) * ld + k0 + t + 4], ah[3], al[3]);
+}
+// the same for A = M^T with M row-major [k][m] (element (m, k) at M[k * ld + m])
+__device__ __forceinline__ void load_at_split(const float* M, int ld, int m0, int k0, uint32_t (&ah)[4], uint32_t (&al)[4]) {
+    const int g = (threadIdx.x & 31) >> 2, t = threadIdx.x & 3;
+    tf32_split(M[(k0 + t) * ld + m0 + g], ah[0], al[0]);
+    tf32_split(M[(k0 + t) * ld + m0 + g + 8], ah[1], al[1]);
+    tf32_split(M[(k0 + t + 4) * ld + m0 + g], ah[2], al[2]);
+    tf32_split(M[(k0 + t + 4) * ld + m0 + g + 8], ah[3], al[3]);
+}
+
+// ---- chunk-local part of the gated delta rule: one CTA (16 warps) per (chunk, head) --------------
 // Per chunk of 64 tokens (zero padded): gc = cumsum(g); T = (I + tril(-(k beta) k^T * decay, -1))^-1 by forward
-// substitution; vprime = T (v beta); kcd = T (k beta exp(gc)); aqk = tril(q k^T * decay).  All f32.
+// substitution; vprime = T (v beta); kcd = T (k beta exp(gc)); aqk = tril(q k^T * decay).  f32 throughout; the four
+// matrix products (k k^T, q k^T, T v, T k) are 3xTF32 tensor-core tiles, the triangular solve stays on the CUDA cores.
 struct ChunkScratch {          // one record per (head, chunk), floats; every array starts on a 16-byte boundary
     float vprime[DN_CHUNK][DN_V];
     float kcd[DN_CHUNK][DN_K];
@@ -153,27 +197,26 @@ struct ChunkScratch {          // one record per (head, chunk), floats; every ar
 };
 
 constexpr int CL_THREADS = 512;
-constexpr int CL_LD = DN_K + 4;                          // padded rows: float4 loads, conflict-free for rows 16 apart
-constexpr int CL_LDA = DN_CHUNK + 1;
-constexpr int CHUNK_LOCAL_SMEM = (3 * DN_CHUNK * CL_LD + DN_CHUNK * CL_LDA + 3 * DN_CHUNK) * 4;
-
-__device__ __forceinline__ float dot4(const float4 a, const float4 b, float acc) {
-    acc = fmaf(a.x, b.x, acc); acc = fmaf(a.y, b.y, acc); acc = fmaf(a.z, b.z, acc); return fmaf(a.w, b.w, acc);
-}
+constexpr int CL_LD = DN_K + 4;                          // q, k: A operands (row-major) and, for k, the transposed B operand: bank = 4 g + t
+constexpr int CL_LDB = DN_K + 8;                         // v beta, k beta exp(gc): B operands [token][dim]: bank = 8 t + g
+constexpr int CL_LDA = DN_CHUNK + 4;                     // T: A operand of the last two products
+constexpr int CHUNK_LOCAL_SMEM = (2 * DN_CHUNK * CL_LD + 2 * DN_CHUNK * CL_LDB + DN_CHUNK * CL_LDA + 3 * DN_CHUNK) * 4;
 
 static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(const bf16* __restrict__ qkv, const float* __restrict__ beta,
                                                                        const float* __restrict__ g, ChunkScratch* __restrict__ scratch,
                                                                        int S, int nchunks) {
     pdl_wait();
     extern __shared__ __align__(16) float sm[];
-    float* sq = sm;                                  // [64][CL_LD]  q / sqrt(128); later k * beta * exp(gc)
-    float* sk = sq + DN_CHUNK * CL_LD;               // [64][CL_LD]  k
-    float* sv = sk + DN_CHUNK * CL_LD;               // [64][CL_LD]  v * beta
-    float* sa = sv + DN_CHUNK * CL_LD;               // [64][CL_LDA]
+    float* sq = sm;                                  // [64][CL_LD]   q / sqrt(128)
+    float* sk = sq + DN_CHUNK * CL_LD;               // [64][CL_LD]   k
+    float* sv = sk + DN_CHUNK * CL_LD;               // [64][CL_LDB]  v * beta
+    float* skb = sv + DN_CHUNK * CL_LDB;             // [64][CL_LDB]  k * beta * exp(gc)
+    float* sa = skb + DN_CHUNK * CL_LDB;             // [64][CL_LDA]  A, then T
     float* sb = sa + DN_CHUNK * CL_LDA;
     float* sg = sb + DN_CHUNK;      // cumulative log-decay
     float* se = sg + DN_CHUNK;      // exp(gc)
-    const int c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    const int c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int gq = lane >> 2, t4 = lane & 3;
     const int t0 = c * DN_CHUNK;
     ChunkScratch& out = scratch[(size_t)h * nchunks + c];
 
@@ -191,7 +234,7 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
             kv = bf2f(row[DN_QK_SIZE]);
             vv = bf2f(row[2 * DN_QK_SIZE]);
         }
-        sq[i * CL_LD + d] = qv; sk[i * CL_LD + d] = kv; sv[i * CL_LD + d] = vv;
+        sq[i * CL_LD + d] = qv; sk[i * CL_LD + d] = kv; sv[i * CL_LDB + d] = vv;
     }
     __syncthreads();
     if (tid == 0) {                 // sequential cumsum, as torch.cumsum does
@@ -200,57 +243,66 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
     }
     __syncthreads();
     if (tid < DN_CHUNK) { se[tid] = expf(sg[tid]); out.gc[tid] = sg[tid]; }
-    for (int e = tid; e < DN_CHUNK * DN_V; e += CL_THREADS) sv[(e >> 7) * CL_LD + (e & 127)] *= sb[e >> 7];      // v * beta
     __syncthreads();
-    {   // operands of the scan that depend on this chunk only
+    {   // operands of the scan that depend on this chunk only; v * beta and k * beta * exp(gc) for the products below
         const float g_last = sg[DN_CHUNK - 1];
         for (int e = tid; e < DN_CHUNK * DN_K; e += CL_THREADS) {
             const int i = e >> 7, d = e & 127;
+            const float kv = sk[i * CL_LD + d];
             out.qs[i][d] = sq[i * CL_LD + d] * se[i];
-            out.ks[i][d] = sk[i * CL_LD + d] * expf(g_last - sg[i]);
+            out.ks[i][d] = kv * expf(g_last - sg[i]);
+            sv[i * CL_LDB + d] *= sb[i];
+            skb[i * CL_LDB + d] = (kv * sb[i]) * se[i];
         }
         if (tid == 0) out.eg_last[0] = expf(g_last);
     }
-    // A[i][j] = -(beta_i k_i . k_j) * exp(gc_i - gc_j) for j < i, else 0;   aqk[i][j] = (q_i . k_j) * exp(gc_i - gc_j) for j <= i
-    // register tile per thread: rows bi, bi + 32 x columns bj, bj + 16, bj + 32, bj + 48 (rows 16 apart: conflict-free float4 loads)
+    // ---- k k^T and q k^T (64 x 64 x 128): only the tiles on and below the diagonal.  A = rows of k (warps 0-7) or q (8-15),
+    // B = k^T.  Eight warps share the 20 lower-triangular 16 x 8 ... tiles of one product: (row tile, first column tile, count)
     {
-        const int bi = tid >> 4, bj = tid & 15;
-        float kk[2][4], qk[2][4];
+        const int u = warp & 7;
+        const int mt = (u < 3) ? 3 : (u < 5) ? 2 : (u < 7) ? 1 : 0;
+        const int nt0 = (u == 1 || u == 4) ? 3 : (u == 2) ? 6 : (u == 6) ? 2 : 0;
+        const int ntn = (u == 2 || u >= 5) ? 2 : 3;
+        const bool is_q = warp >= 8;
+        const float* A = is_q ? sq : sk;
+        float acc[3][4];
 #pragma unroll
-        for (int r = 0; r < 2; ++r)
+        for (int n = 0; n < 3; ++n)
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) { kk[r][cc] = 0.f; qk[r][cc] = 0.f; }
+            for (int r = 0; r < 4; ++r) acc[n][r] = 0.f;
 #pragma unroll 2
-        for (int d = 0; d < DN_K; d += 4) {
-            float4 ki[2], qi[2], kj[4];
+        for (int k0 = 0; k0 < DN_K; k0 += 8) {
+            uint32_t ah[4], al[4];
+            load_a_split(A, CL_LD, mt * 16, k0, ah, al);
 #pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                ki[r] = *reinterpret_cast<const float4*>(sk + (bi + 32 * r) * CL_LD + d);
-                qi[r] = *reinterpret_cast<const float4*>(sq + (bi + 32 * r) * CL_LD + d);
-            }
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) kj[cc] = *reinterpret_cast<const float4*>(sk + (bj + 16 * cc) * CL_LD + d);
-#pragma unroll
-            for (int r = 0; r < 2; ++r)
-#pragma unroll
-                for (int cc = 0; cc < 4; ++cc) { kk[r][cc] = dot4(ki[r], kj[cc], kk[r][cc]); qk[r][cc] = dot4(qi[r], kj[cc], qk[r][cc]); }
+            for (int n = 0; n < 3; ++n)
+                if (n < ntn) {
+                    const float* br = sk + ((nt0 + n) * 8 + gq) * CL_LD + k0 + t4;        // B(k, n) = k[token n][dim k]
+                    uint32_t bh0, bl0, bh1, bl1;
+                    tf32_split(br[0], bh0, bl0);
+                    tf32_split(br[4], bh1, bl1);
+                    mma_3xtf32(acc[n], ah, al, bh0, bh1, bl0, bl1);
+                }
         }
+        // A[i][j] = -(beta_i k_i . k_j) * exp(gc_i - gc_j) for j < i, else 0;   aqk[i][j] = (q_i . k_j) * exp(gc_i - gc_j) for j <= i
 #pragma unroll
-        for (int r = 0; r < 2; ++r)
+        for (int n = 0; n < 3; ++n)
+            if (n < ntn)
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                const int i = bi + 32 * r, j = bj + 16 * cc;
-                const float dec = (j <= i) ? expf(sg[i] - sg[j]) : 0.f;
-                sa[i * CL_LDA + j] = (j < i) ? -((kk[r][cc] * sb[i]) * dec) : 0.f;
-                out.aqk[i][j] = (j <= i) ? qk[r][cc] * dec : 0.f;
-            }
+                for (int r = 0; r < 4; ++r) {
+                    const int i = mt * 16 + gq + 8 * (r >> 1), j = (nt0 + n) * 8 + 2 * t4 + (r & 1);
+                    const float dec = (j <= i) ? expf(sg[i] - sg[j]) : 0.f;
+                    if (is_q) out.aqk[i][j] = (j <= i) ? acc[n][r] * dec : 0.f;
+                    else sa[i * CL_LDA + j] = (j < i) ? -((acc[n][r] * sb[i]) * dec) : 0.f;
+                }
+        // the tiles above the diagonal blocks were not computed: aqk and A are zero there (the forward substitution reads
+        // column entries above the diagonal and relies on their being zero)
+        for (int e = tid; e < DN_CHUNK * DN_CHUNK; e += CL_THREADS) {
+            const int i = e >> 6, j = e & 63;
+            if ((j >> 4) > (i >> 4)) { out.aqk[i][j] = 0.f; sa[i * CL_LDA + j] = 0.f; }
+        }
     }
     __syncthreads();
-    // k * beta * exp(gc) replaces q (no longer needed)
-    for (int e = tid; e < DN_CHUNK * DN_K; e += CL_THREADS) {
-        const int i = e >> 7, d = e & 127;
-        sq[i * CL_LD + d] = (sk[i * CL_LD + d] * sb[i]) * se[i];
-    }
     // forward substitution, row by row: row_i[:i] += sum_{j<i} row_i[j] * A[j][:i]  (rows j < i already final).
     // Only 64 threads take part, so the 126 hand-offs use a 64-thread named barrier; the other warps wait below.
     if (tid < DN_CHUNK) {
@@ -279,44 +331,60 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
     __syncthreads();
     if (tid < DN_CHUNK) sa[tid * CL_LDA + tid] = 1.0f;
     __syncthreads();
-    // vprime = T (v beta);  kcd = T (k beta exp(gc)).  thread: four columns, rows ig, ig + 16, ig + 32, ig + 48; T is zero above
-    // its diagonal, so every row runs over the same j range
+    // ---- vprime = T (v beta) (warps 0-7), kcd = T (k beta exp(gc)) (warps 8-15): 64 x 128 x 64 with T lower triangular.  A warp
+    // takes a quarter of the 128 columns and two row tiles whose k ranges add up to the same length: (0, 3) or (1, 2).
     {
-        const int d4 = (tid & 31) * 4, ig = tid >> 5;
-        float av[4][4], ak[4][4];
+        const int u = warp & 7, nq = u & 3;
+        const float* Bm = (warp < 8) ? sv : skb;
+        float (*dst)[DN_K] = (warp < 8) ? out.vprime : out.kcd;
 #pragma unroll
-        for (int r = 0; r < 4; ++r)
+        for (int pass = 0; pass < 2; ++pass) {
+            const int mt = (u < 4) ? (pass ? 3 : 0) : (pass ? 2 : 1);
+            float acc[4][4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) { av[r][u] = 0.f; ak[r][u] = 0.f; }
-        const int jmax = ig + 48;
-        for (int j = 0; j <= jmax; ++j) {
-            const float4 v4 = *reinterpret_cast<const float4*>(sv + j * CL_LD + d4);
-            const float4 k4 = *reinterpret_cast<const float4*>(sq + j * CL_LD + d4);
+            for (int n = 0; n < 4; ++n)
 #pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const float tv = sa[(ig + 16 * r) * CL_LDA + j];
-                av[r][0] = fmaf(tv, v4.x, av[r][0]); av[r][1] = fmaf(tv, v4.y, av[r][1]); av[r][2] = fmaf(tv, v4.z, av[r][2]); av[r][3] = fmaf(tv, v4.w, av[r][3]);
-                ak[r][0] = fmaf(tv, k4.x, ak[r][0]); ak[r][1] = fmaf(tv, k4.y, ak[r][1]); ak[r][2] = fmaf(tv, k4.z, ak[r][2]); ak[r][3] = fmaf(tv, k4.w, ak[r][3]);
+                for (int r = 0; r < 4; ++r) acc[n][r] = 0.f;
+            for (int k0 = 0; k0 < 16 * (mt + 1); k0 += 8) {
+                uint32_t ah[4], al[4];
+                load_a_split(sa, CL_LDA, mt * 16, k0, ah, al);
+#pragma unroll
+                for (int n = 0; n < 4; ++n) {
+                    const float* br = Bm + (k0 + t4) * CL_LDB + nq * 32 + n * 8 + gq;       // B(k, n) = Bm[token k][dim n]
+                    uint32_t bh0, bl0, bh1, bl1;
+                    tf32_split(br[0], bh0, bl0);
+                    tf32_split(br[4 * CL_LDB], bh1, bl1);
+                    mma_3xtf32(acc[n], ah, al, bh0, bh1, bl0, bl1);
+                }
             }
-        }
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            *reinterpret_cast<float4*>(&out.vprime[ig + 16 * r][d4]) = make_float4(av[r][0], av[r][1], av[r][2], av[r][3]);
-            *reinterpret_cast<float4*>(&out.kcd[ig + 16 * r][d4]) = make_float4(ak[r][0], ak[r][1], ak[r][2], ak[r][3]);
+            for (int n = 0; n < 4; ++n)
+#pragma unroll
+                for (int hr = 0; hr < 2; ++hr)
+                    *reinterpret_cast<float2*>(&dst[mt * 16 + gq + 8 * hr][nq * 32 + n * 8 + 2 * t4]) = make_float2(acc[n][2 * hr], acc[n][2 * hr + 1]);
         }
     }
 }
 
-// ---- scan over chunks: one CTA (512 threads) per (head, 16-wide slice of the value dimension) --------
+// ---- scan over chunks: one CTA (8 warps) per (head, 16-wide slice of the value dimension) --------
 // Sequential over the chunks of a head; per chunk  v_new = vprime - kcd S,  out = qs S + aqk v_new,
-// S <- S exp(gc_last) + ks^T v_new  (S = state slice [128 k][16 v] in shared memory, all f32).  The operands are
-// plain copies of what the chunk-local kernel wrote, so they arrive by cp.async while the previous phase computes:
-// group 1 = {kcd, qs, vprime slice} (first phase), group 2 = {aqk, ks} (second and third), each refilled as soon
-// as its buffers are free.
+// S <- S exp(gc_last) + ks^T v_new  (S = state slice [128 k][16 v]).  All four products run on the tensor cores as
+// 3xTF32 mma.sync tiles:
+//   P1  warps 0-3: VP = kcd S, warps 4-7: IT = qs S      (64 x 128 x 16, one 16-row tile and both 8-column tiles per warp)
+//   P2  warps 4-7: out = IT + aqk v_new                   (64 x 64 x 16, lower-triangular: zero k-steps skipped)
+//   P3  all warps: S' = S exp(gc_last) + ks^T v_new       (128 x 64 x 16, one 16-row tile per warp)
+// The state slice lives in registers as the f32 accumulator fragment of P3 from chunk to chunk (no precision is lost to
+// the operand split); shared memory holds its hi / lo split as the B operand of the next chunk's P1, and v_new likewise.
+// The left operands are plain copies of what the chunk-local kernel wrote and arrive by cp.async while the previous phase
+// computes: group 1 = {kcd, qs, vprime slice}, group 2 = {aqk, ks}, each refilled as soon as its buffers are free.
 constexpr int SCAN_VW = 16;
-constexpr int SCAN_THREADS = 512;
-constexpr int SCAN_LDK = DN_K + 4, SCAN_LDA = DN_CHUNK + 4;       // padded rows: 16-byte aligned and conflict-free
-constexpr int CHUNK_SCAN_SMEM = (3 * DN_CHUNK * SCAN_LDK + DN_CHUNK * SCAN_LDA + 2 * DN_CHUNK * SCAN_VW + DN_K * SCAN_VW) * 4;
+constexpr int SCAN_THREADS = 256;
+constexpr int SCAN_LDA = DN_K + 4;          // kcd, qs: row-major A operands, bank = 4 g + t
+constexpr int SCAN_LDT = DN_K + 8;          // ks: read as its transpose, bank = 8 t + g
+constexpr int SCAN_LDQ = DN_CHUNK + 4;      // aqk
+constexpr int SCAN_LDB = SCAN_VW + 8;       // B operands (state and v_new, hi and lo): bank = 24 t + g
+constexpr int CHUNK_SCAN_SMEM = (2 * DN_CHUNK * SCAN_LDA + DN_CHUNK * SCAN_LDT + DN_CHUNK * SCAN_LDQ + DN_CHUNK * SCAN_VW +
+                                 2 * DN_K * SCAN_LDB + 2 * DN_CHUNK * SCAN_LDB) * 4;
 
 __device__ __forceinline__ void scan_cp16(float* dst, const float* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src) : "memory");
@@ -326,24 +394,27 @@ static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(c
                                                                         float* __restrict__ state_out, int S, int nchunks) {
     pdl_wait();
     extern __shared__ __align__(16) float sm[];
-    float* skcd = sm;                                   // [64][SCAN_LDK]
-    float* sq = skcd + DN_CHUNK * SCAN_LDK;             // [64][SCAN_LDK]
-    float* sk = sq + DN_CHUNK * SCAN_LDK;               // [64][SCAN_LDK]
-    float* sa = sk + DN_CHUNK * SCAN_LDK;               // [64][SCAN_LDA]
-    float* svp = sa + DN_CHUNK * SCAN_LDA;              // [64][16]
-    float* svn = svp + DN_CHUNK * SCAN_VW;              // [64][16]
-    float* sst = svn + DN_CHUNK * SCAN_VW;              // [128][16] state slice [k][v]
-    const int h = blockIdx.x, vs = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
+    float* skcd = sm;                                   // [64][SCAN_LDA]
+    float* sq = skcd + DN_CHUNK * SCAN_LDA;             // [64][SCAN_LDA]
+    float* sk = sq + DN_CHUNK * SCAN_LDA;               // [64][SCAN_LDT]
+    float* sa = sk + DN_CHUNK * SCAN_LDT;               // [64][SCAN_LDQ]
+    float* svp = sa + DN_CHUNK * SCAN_LDQ;              // [64][16]
+    uint32_t* sth = reinterpret_cast<uint32_t*>(svp + DN_CHUNK * SCAN_VW);   // [128][SCAN_LDB] state, tf32 hi
+    uint32_t* stl = sth + DN_K * SCAN_LDB;                                   //                  state, tf32 lo
+    uint32_t* vnh = stl + DN_K * SCAN_LDB;                                   // [64][SCAN_LDB]  v_new, tf32 hi
+    uint32_t* vnl = vnh + DN_CHUNK * SCAN_LDB;                               //                  v_new, tf32 lo
+    const int h = blockIdx.x, vs = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t4 = lane & 3;
     const int v0 = vs * SCAN_VW;
-    for (int e = tid; e < DN_K * SCAN_VW; e += SCAN_THREADS) sst[e] = 0.f;
+    for (int e = tid; e < 2 * DN_K * SCAN_LDB; e += SCAN_THREADS) sth[e] = 0u;          // state = 0 (hi and lo)
 
     auto issue_g1 = [&](int c) {
         if (c < nchunks) {
             const ChunkScratch& in = scratch[(size_t)h * nchunks + c];
             for (int e = tid; e < DN_CHUNK * (DN_K / 4); e += SCAN_THREADS) {
                 const int i = e >> 5, q4 = (e & 31) * 4;
-                scan_cp16(skcd + i * SCAN_LDK + q4, &in.kcd[i][q4]);
-                scan_cp16(sq + i * SCAN_LDK + q4, &in.qs[i][q4]);
+                scan_cp16(skcd + i * SCAN_LDA + q4, &in.kcd[i][q4]);
+                scan_cp16(sq + i * SCAN_LDA + q4, &in.qs[i][q4]);
             }
             for (int e = tid; e < DN_CHUNK * (SCAN_VW / 4); e += SCAN_THREADS) {
                 const int i = e >> 2, q4 = (e & 3) * 4;
@@ -357,11 +428,11 @@ static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(c
             const ChunkScratch& in = scratch[(size_t)h * nchunks + c];
             for (int e = tid; e < DN_CHUNK * (DN_K / 4); e += SCAN_THREADS) {
                 const int i = e >> 5, q4 = (e & 31) * 4;
-                scan_cp16(sk + i * SCAN_LDK + q4, &in.ks[i][q4]);
+                scan_cp16(sk + i * SCAN_LDT + q4, &in.ks[i][q4]);
             }
             for (int e = tid; e < DN_CHUNK * (DN_CHUNK / 4); e += SCAN_THREADS) {
                 const int i = e >> 4, q4 = (e & 15) * 4;
-                scan_cp16(sa + i * SCAN_LDA + q4, &in.aqk[i][q4]);
+                scan_cp16(sa + i * SCAN_LDQ + q4, &in.aqk[i][q4]);
             }
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
@@ -369,84 +440,118 @@ static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(c
     issue_g1(0);
     issue_g2(0);
 
+    // this warp's 16 x 16 piece of the state (rows = keys 16 warp .., columns = the slice's 16 values), f32, in registers
+    float st[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) st[nt][r] = 0.f;
+
     for (int c = 0; c < nchunks; ++c) {
         const int t0 = c * DN_CHUNK;
         const float dec = scratch[(size_t)h * nchunks + c].eg_last[0];
         asm volatile("cp.async.wait_group 1;" ::: "memory");          // group 1 of this chunk has landed
-        __syncthreads();
-        // phase 1: v_new = vprime - kcd S ; inter = qs S.   thread: row i, four value columns, half of the key range
-        const int i = tid >> 3, vq = ((tid >> 1) & 3) * 4, kh = tid & 1;
-        float vp[4] = {0.f, 0.f, 0.f, 0.f}, it[4] = {0.f, 0.f, 0.f, 0.f};
+        __syncthreads();                                               // ... for everybody; the state split of the previous chunk is complete
+        // ---- P1: VP = kcd S (warps 0-3), IT = qs S (warps 4-7) ----
+        const int mt = warp & 3, m0 = mt * 16;
+        float acc[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) acc[nt][r] = 0.f;
         {
-            const float* ar = skcd + i * SCAN_LDK + kh;                 // keys kh, kh + 2, ...: the two halves hit different banks
-            const float* br = sq + i * SCAN_LDK + kh;
-            const float* sr = sst + kh * SCAN_VW + vq;
-#pragma unroll 8
-            for (int d = 0; d < DN_K / 2; ++d) {
-                const float4 s4 = *reinterpret_cast<const float4*>(sr + 2 * d * SCAN_VW);
-                const float a = ar[2 * d], b = br[2 * d];
-                vp[0] = fmaf(a, s4.x, vp[0]); vp[1] = fmaf(a, s4.y, vp[1]); vp[2] = fmaf(a, s4.z, vp[2]); vp[3] = fmaf(a, s4.w, vp[3]);
-                it[0] = fmaf(b, s4.x, it[0]); it[1] = fmaf(b, s4.y, it[1]); it[2] = fmaf(b, s4.z, it[2]); it[3] = fmaf(b, s4.w, it[3]);
-            }
+            const float* A = (warp < 4) ? skcd : sq;
+#pragma unroll 4
+            for (int k0 = 0; k0 < DN_K; k0 += 8) {
+                uint32_t ah[4], al[4];
+                load_a_split(A, SCAN_LDA, m0, k0, ah, al);
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                vp[u] += __shfl_xor_sync(0xffffffffu, vp[u], 1);
-                it[u] += __shfl_xor_sync(0xffffffffu, it[u], 1);
+                for (int nt = 0; nt < 2; ++nt) {
+                    const int bi0 = (k0 + t4) * SCAN_LDB + nt * 8 + g, bi1 = bi0 + 4 * SCAN_LDB;
+                    mma_3xtf32(acc[nt], ah, al, sth[bi0], sth[bi1], stl[bi0], stl[bi1]);
+                }
             }
-            if (kh == 0) {
+        }
+        if (warp < 4) {
+            // v_new = vprime - VP, stored split as the B operand of P2 and P3
 #pragma unroll
-                for (int u = 0; u < 4; ++u) svn[i * SCAN_VW + vq + u] = svp[i * SCAN_VW + vq + u] - vp[u];
-            }
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const int row = m0 + g + 8 * (r >> 1), col = nt * 8 + 2 * t4 + (r & 1);
+                    uint32_t hi, lo;
+                    tf32_split(svp[row * SCAN_VW + col] - acc[nt][r], hi, lo);
+                    vnh[row * SCAN_LDB + col] = hi;
+                    vnl[row * SCAN_LDB + col] = lo;
+                }
         }
         __syncthreads();                                               // v_new complete; kcd / qs / vprime buffers are free
         issue_g1(c + 1);
         asm volatile("cp.async.wait_group 1;" ::: "memory");          // group 2 of this chunk has landed
         __syncthreads();
-        // phase 2: out = inter + aqk v_new   (the two key-halves of a row split the j range)
-        {
-            float o[4] = {0.f, 0.f, 0.f, 0.f};
-            const float* ar = sa + i * SCAN_LDA;
-            for (int j = kh; j <= i; j += 2) {
-                const float a = ar[j];
-                const float4 n4 = *reinterpret_cast<const float4*>(svn + j * SCAN_VW + vq);
-                o[0] = fmaf(a, n4.x, o[0]); o[1] = fmaf(a, n4.y, o[1]); o[2] = fmaf(a, n4.z, o[2]); o[3] = fmaf(a, n4.w, o[3]);
+        // ---- P2 (warps 4-7): out = IT + aqk v_new; aqk is lower triangular, so row tile mt needs tokens j < 16 (mt + 1) only ----
+        if (warp >= 4) {
+            for (int k0 = 0; k0 < 16 * (mt + 1); k0 += 8) {
+                uint32_t ah[4], al[4];
+                load_a_split(sa, SCAN_LDQ, m0, k0, ah, al);
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
+                    const int bi0 = (k0 + t4) * SCAN_LDB + nt * 8 + g, bi1 = bi0 + 4 * SCAN_LDB;
+                    mma_3xtf32(acc[nt], ah, al, vnh[bi0], vnh[bi1], vnl[bi0], vnl[bi1]);
+                }
             }
 #pragma unroll
-            for (int u = 0; u < 4; ++u) o[u] += __shfl_xor_sync(0xffffffffu, o[u], 1);
-            const int t = t0 + i;
-            if (kh == 0 && t < S) {
-                bf16* dst = core_out + (size_t)t * DN_V_SIZE + h * DN_V + v0 + vq;
-                *reinterpret_cast<__nv_bfloat162*>(dst) = __halves2bfloat162(f2bf(it[0] + o[0]), f2bf(it[1] + o[1]));
-                *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __halves2bfloat162(f2bf(it[2] + o[2]), f2bf(it[3] + o[3]));
-            }
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                for (int hr = 0; hr < 2; ++hr) {
+                    const int tok = t0 + m0 + g + 8 * hr;
+                    if (tok < S) {
+                        bf16* dst = core_out + (size_t)tok * DN_V_SIZE + h * DN_V + v0 + nt * 8 + 2 * t4;
+                        *reinterpret_cast<__nv_bfloat162*>(dst) = __halves2bfloat162(f2bf(acc[nt][2 * hr]), f2bf(acc[nt][2 * hr + 1]));
+                    }
+                }
         }
-        // phase 3: S = S exp(gc_last) + ks^T v_new.   thread: key d, four value columns
+        // ---- P3 (all warps): S' = S exp(gc_last) + ks^T v_new; this warp owns state rows (keys) 16 warp .. 16 warp + 15 ----
         {
-            const int d = tid >> 2, vo = (tid & 3) * 4;
-            float acc[4];
-            const float4 s4 = *reinterpret_cast<const float4*>(sst + d * SCAN_VW + vo);
-            acc[0] = s4.x * dec; acc[1] = s4.y * dec; acc[2] = s4.z * dec; acc[3] = s4.w * dec;
-#pragma unroll 8
-            for (int j = 0; j < DN_CHUNK; ++j) {
-                const float kw = sk[j * SCAN_LDK + d];
-                const float4 n4 = *reinterpret_cast<const float4*>(svn + j * SCAN_VW + vo);
-                acc[0] = fmaf(kw, n4.x, acc[0]); acc[1] = fmaf(kw, n4.y, acc[1]); acc[2] = fmaf(kw, n4.z, acc[2]); acc[3] = fmaf(kw, n4.w, acc[3]);
+            const int d0 = warp * 16;
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) st[nt][r] *= dec;
+#pragma unroll 4
+            for (int k0 = 0; k0 < DN_CHUNK; k0 += 8) {
+                uint32_t ah[4], al[4];
+                load_at_split(sk, SCAN_LDT, d0, k0, ah, al);
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
+                    const int bi0 = (k0 + t4) * SCAN_LDB + nt * 8 + g, bi1 = bi0 + 4 * SCAN_LDB;
+                    mma_3xtf32(st[nt], ah, al, vnh[bi0], vnh[bi1], vnl[bi0], vnl[bi1]);
+                }
             }
-            // each thread reads and writes only its own four state words here; phase 1 of the next chunk reads them
-            // all, after the barrier at the top of the loop
-            *reinterpret_cast<float4*>(sst + d * SCAN_VW + vo) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            // the new state, split, for the next chunk's P1 (only this warp reads or writes these rows before the barrier)
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const int row = d0 + g + 8 * (r >> 1), col = nt * 8 + 2 * t4 + (r & 1);
+                    uint32_t hi, lo;
+                    tf32_split(st[nt][r], hi, lo);
+                    sth[row * SCAN_LDB + col] = hi;
+                    stl[row * SCAN_LDB + col] = lo;
+                }
         }
-        __syncthreads();                                               // aqk / ks buffers are free
+        __syncthreads();                                               // aqk / ks / v_new buffers are free
         issue_g2(c + 1);
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();
-    // final state in the reference layout [head][v][k]
-    for (int e = tid; e < DN_K * SCAN_VW; e += SCAN_THREADS) {
-        const int v = e / DN_K, d = e % DN_K;
-        state_out[((size_t)h * DN_V + v0 + v) * DN_K + d] = sst[d * SCAN_VW + v];
-    }
-    (void)lane;
+    // final state in the reference layout [head][v][k], from the f32 registers
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int d = warp * 16 + g + 8 * (r >> 1), v = nt * 8 + 2 * t4 + (r & 1);
+            state_out[((size_t)h * DN_V + v0 + v) * DN_K + d] = st[nt][r];
+        }
 }
 
 // ---- gated RMSNorm of the DeltaNet output: one warp per (token, head) --------------------------------

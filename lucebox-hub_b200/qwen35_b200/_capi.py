@@ -8,7 +8,8 @@ import ctypes as C
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libqwen35_b200.so")
+# QWEN35_B200_LIB selects another build of the same library (kernel experiments); the default is the in-tree build
+LIB_PATH = os.environ.get("QWEN35_B200_LIB") or os.path.join(_HERE, "libqwen35_b200.so")
 
 OK = 0
 STATUS_NAMES = {0: "ok", 1: "device wait timed out", 2: "bad argument", 3: "CUDA error", 4: "unsupported"}
@@ -132,6 +133,9 @@ SIGNATURES = {
     "qwen35_b200_dequant_q4k": (_i, [_vp, C.c_size_t, _vp, _vp, _vp]),
     "qwen35_b200_gemm_bf16": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "qwen35_b200_gemm_q4k": (_i, [_vp, _i, _vp, _i, _vp, _i, _vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "qwen35_b200_nvfp4_act_bytes": (C.c_size_t, [_i, _i, C.POINTER(C.c_size_t)]),
+    "qwen35_b200_quantize_act_nvfp4": (_i, [_vp, _i, _i, _vp, _vp, _vp]),
+    "qwen35_b200_gemm_nvfp4": (_i, [_vp, _vp, _i, _vp, _vp, _i, _i, C.c_float, _vp, _i, _i, _vp, _i, _vp]),
     "qwen35_b200_status": (_i, [_vp]),
     "qwen35_b200_clear_status": (_i, [_vp]),
     "qwen35_b200_workspace_if_any": (_vp, []),

@@ -1,4 +1,9 @@
-"""GPU parity of the NVFP4 packers against the numpy oracle, bit for bit, through the C ABI."""
+"""GPU parity of the NVFP4 packers, through the C ABI: byte for byte against the reference's own kernels (compiled from
+its source with its flags, oracle/_ref), and against the numpy oracle, which restates the arithmetic in IEEE operations.
+The reference builds with fast-math, whose approximate reciprocal sits one f32 last place from the IEEE quotient for
+some scales; an element that falls exactly on a threshold of the E2M1 grid then takes the neighbouring code.  Against
+the IEEE oracle the comparison therefore allows a handful of neighbouring codes (and fp16 scales one last place apart);
+against the reference's kernels it allows nothing."""
 import numpy as np
 import pytest
 import torch
@@ -21,14 +26,35 @@ def _mats():
     return [a, b, c]
 
 
+def _assert_codes_close(got, ref, what, max_frac=2e-4):
+    """Packed E2M1 bytes: identical except for at most max_frac of the nibbles, each of which is the neighbouring code."""
+    got, ref = np.asarray(got), np.asarray(ref)
+    assert got.shape == ref.shape, what
+    g = np.stack([got & 0xF, got >> 4], -1).astype(np.int32)
+    r = np.stack([ref & 0xF, ref >> 4], -1).astype(np.int32)
+    bad = g != r
+    frac = float(bad.mean())
+    assert frac <= max_frac, (what, frac)
+    if bad.any():
+        gm, rm = g[bad] & 7, r[bad] & 7
+        assert bool((np.abs(gm - rm) <= 1).all()), what               # neighbouring magnitudes
+        assert bool((((g[bad] ^ r[bad]) & 8) == 0).all() | ((gm == 0) | (rm == 0)).all()), what
+    return frac
+
+
+def _assert_half_scales_close(got_u16, ref_u16, what, max_frac=2e-3):
+    d = np.abs(got_u16.astype(np.int32) - ref_u16.astype(np.int32))
+    assert int(d.max()) <= 1 and float((d > 0).mean()) <= max_frac, (what, int(d.max()), float((d > 0).mean()))
+
+
 @pytest.mark.parametrize("idx", [0, 1, 2])
 def test_tensor_core_layout_bit_exact(idx):
     from qwen35_b200.model import _quantize_matrix_nvfp4_lm
     w = torch.from_numpy(_mats()[idx]).bfloat16()
     ref_p, ref_s = R.quantize_nvfp4_lm(w.float().numpy())
     got = _quantize_matrix_nvfp4_lm(w.cuda())
-    assert np.array_equal(got["packed"].cpu().numpy(), ref_p)
-    assert np.array_equal(got["scales"].cpu().numpy(), ref_s)
+    _assert_codes_close(got["packed"].cpu().numpy(), ref_p, ("tc packed", idx))
+    assert np.array_equal(got["scales"].cpu().numpy(), ref_s)          # amax * (1/6) and the E4M3 conversion are exact either way
 
 
 @pytest.mark.parametrize("idx,group", [(0, 32), (1, 32), (2, 32), (0, 16), (1, 64)])
@@ -37,8 +63,8 @@ def test_decode_body_layout_bit_exact(idx, group):
     w = torch.from_numpy(_mats()[idx]).bfloat16()
     ref_p, ref_s = R.quantize_nvfp4(w.float().numpy(), group)
     got = _quantize_matrix_nvfp4(w.cuda(), group)
-    assert np.array_equal(got["packed"].cpu().numpy(), ref_p)
-    assert np.array_equal(got["scales"].cpu().numpy().view(np.uint16), ref_s.view(np.uint16))
+    _assert_codes_close(got["packed"].cpu().numpy(), ref_p, ("decode packed", idx, group), max_frac=2e-3)
+    _assert_half_scales_close(got["scales"].cpu().numpy().view(np.uint16), ref_s.view(np.uint16), ("decode scales", idx, group))
 
 
 def test_padded_rows_and_errors():
@@ -47,7 +73,8 @@ def test_padded_rows_and_errors():
     q = _quantize_matrix_nvfp4_tc(w)
     assert q["padded_rows"] == 256 and q["packed"].shape == (256, 64)
     ref_p, ref_s = R.quantize_nvfp4_lm(torch.cat([w.cpu().float(), torch.zeros(56, 128)]).numpy())
-    assert np.array_equal(q["packed"].cpu().numpy(), ref_p) and np.array_equal(q["scales"].cpu().numpy(), ref_s)
+    _assert_codes_close(q["packed"].cpu().numpy(), ref_p, "padded tc packed")
+    assert np.array_equal(q["scales"].cpu().numpy(), ref_s)
     with pytest.raises(ValueError):
         _quantize_matrix_nvfp4_lm(w)                      # 200 rows
     with pytest.raises(ValueError):
@@ -100,8 +127,8 @@ def test_packers_equal_the_reference_kernels_byte_for_byte(full_weights_cpu):
             p = torch.zeros_like(mine["packed"]); s = torch.zeros_like(mine["scales"])
             ref.launch_quantize_nvfp4_out(w.data_ptr(), rows, cols, group, p.data_ptr(), s.data_ptr(), st)
             torch.cuda.synchronize()
-            assert torch.equal(p, mine["packed"]), (tuple(w.shape), group, "packed")
-            assert torch.equal(s.view(torch.int16), mine["scales"].view(torch.int16)), (tuple(w.shape), group, "scales")
+            assert torch.equal(p, mine["packed"]), (tuple(w.shape), group, "packed", int((p != mine["packed"]).sum()), p.numel())
+            assert torch.equal(s.view(torch.int16), mine["scales"].view(torch.int16)), (tuple(w.shape), group, "scales", int((s.view(torch.int16) != mine["scales"].view(torch.int16)).sum()))
             n_dec += 1
         if rows % 128 == 0 and cols % 64 == 0:
             mine = _quantize_matrix_nvfp4_lm(w)

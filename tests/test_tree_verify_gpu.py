@@ -127,10 +127,12 @@ def test_tree_verify_at_the_27b_widths():
         tt.ssm_state[i] = orc.ssm[i].cuda(); tt.conv_state[i] = orc.conv[i].cuda()
     tt.past = n_ctx
     rng = np.random.default_rng(11)
-    _check_tree_against_oracle(D, orc, tt, rng, random_tree(n_nodes, 8, 11), n_nodes)
+    # at these widths the residual stream is 10-30 in magnitude and a layer sums 5120- to 17408-term products: measured 78 %
+    # of the layer outputs bit-identical (96-100 % at the reduced widths), the rest one last place off
+    _check_tree_against_oracle(D, orc, tt, rng, random_tree(n_nodes, 8, 11), n_nodes, min_exact=0.70, logit_tol=0.07)
 
 
-def _check_tree_against_oracle(D, orc, tt, rng, parents, n_nodes):
+def _check_tree_against_oracle(D, orc, tt, rng, parents, n_nodes, min_exact=0.90, logit_tol=LOGIT_TOL):
     tokens = rng.integers(0, D.vocab, n_nodes)
     ref_logits, ctxs, hids = orc.verify(tokens, parents)
     teacher = torch.zeros(D.n_layers, n_nodes, D.hidden, dtype=torch.bfloat16)
@@ -146,13 +148,19 @@ def _check_tree_against_oracle(D, orc, tt, rng, parents, n_nodes):
     worst_state = 0.0
     for t in range(n_nodes):
         for il in range(D.n_layers):
-            assert float((got_h[il, t] - hids[t][il]).abs().max()) <= LAYER_ABS_TOL, (t, il)
+            # One or two bf16 last places of the LARGEST summand: the layer output is residual + down projection, and where
+            # the two nearly cancel the roundings of the summands (one last place of their magnitude) remain in a small
+            # result.  So the bound follows the row's largest magnitude: 2^-5 where the hidden state is of order 1 (the
+            # reduced widths), 2^-7 of the row maximum on top (at hidden 5120 the residual stream reaches +-30).
+            ref_h = hids[t][il]
+            assert float((got_h[il, t] - ref_h).abs().max()) <= LAYER_ABS_TOL + float(ref_h.abs().max()) * 2.0 ** -7, (t, il)
         for j, il in enumerate(i_dn):
             ref_s = ctxs[t]["ssm"][j]
             got_s = tt.node_states[j, t].float().cpu()
             worst_state = max(worst_state, float((got_s - ref_s).norm() / ref_s.norm().clamp_min(1e-6)))
     exact = float((got_h == torch.stack([torch.stack(h) for h in hids]).transpose(0, 1)).float().mean())
     print(f"teacher forced: {exact:.4%} of layer outputs bit-identical, worst node-state rel error {worst_state:.2e}")
+    assert exact >= min_exact
     assert worst_state <= STATE_REL_TOL
     # free running: logits and arg-max
     logits = torch.zeros(n_nodes, D.vocab, dtype=torch.bfloat16, device="cuda")
@@ -161,9 +169,9 @@ def _check_tree_against_oracle(D, orc, tt, rng, parents, n_nodes):
     got_l = logits.float().cpu()
     for t in range(n_nodes):
         dl = (got_l[t] - ref_logits[t]).abs()
-        assert float(dl.max()) <= LOGIT_TOL, (t, float(dl.max()))
+        assert float(dl.max()) <= logit_tol, (t, float(dl.max()))
         top = torch.topk(ref_logits[t], 2).values
-        if float(top[0] - top[1]) > 2 * LOGIT_TOL:
+        if float(top[0] - top[1]) > 2 * logit_tol:
             assert int(am[t]) == int(ref_logits[t].argmax())
     # accepted path: force arg-max values so that a known root-to-node chain is taken, then commit and compare
     children = {t: [c for c in range(n_nodes) if parents[c] == t] for t in range(n_nodes)}
@@ -187,12 +195,14 @@ def _check_tree_against_oracle(D, orc, tt, rng, parents, n_nodes):
     n_acc = tt.commit()
     orc.commit(ctxs, ref_path)
     assert n_acc == len(ref_path) and tt.past == orc.past
+    def close(got, ref, floor):     # a couple of bf16 last places of the value, with a floor for values near zero
+        return bool(((got - ref).abs() <= ref.abs() * 2.0 ** -6 + floor).all())
     for i in range(D.n_fa):
-        assert float((tt.k_cache[i, :, :tt.past].float().cpu() - orc.k[i]).abs().max()) <= 2.0 ** -5
-        assert float((tt.v_cache[i, :, :tt.past].float().cpu() - orc.v[i]).abs().max()) <= 2.0 ** -5
+        assert close(tt.k_cache[i, :, :tt.past].float().cpu(), orc.k[i], 2.0 ** -5)
+        assert close(tt.v_cache[i, :, :tt.past].float().cpu(), orc.v[i], 2.0 ** -5)
     for j in range(D.n_dn):      # free running here: see the note at STATE_REL_TOL
         assert float((tt.ssm_state[j].cpu() - orc.ssm[j]).norm() / orc.ssm[j].norm().clamp_min(1e-6)) <= 1e-2
-        assert float((tt.conv_state[j].cpu() - orc.conv[j]).abs().max()) <= 2.0 ** -6
+        assert close(tt.conv_state[j].cpu(), orc.conv[j], 2.0 ** -6)
     # a second tree on top of the committed state keeps working (state hand-over through the commit)
     tokens2 = rng.integers(0, D.vocab, 3)
     ref2, _, _ = orc.verify(tokens2, [-1, 0, 0])
@@ -200,7 +210,7 @@ def _check_tree_against_oracle(D, orc, tt, rng, parents, n_nodes):
     tt.verify(torch.tensor(tokens2, dtype=torch.int32), torch.tensor([-1, 0, 0], dtype=torch.int32), logits_out=l2)
     tt.check_status()
     for t in range(3):
-        assert float((l2[t].float().cpu() - ref2[t]).abs().max()) <= 2 * LOGIT_TOL
+        assert float((l2[t].float().cpu() - ref2[t]).abs().max()) <= 2 * logit_tol
 
 
 def test_tree_verify_argument_checks():
