@@ -50,7 +50,10 @@ static_assert(sizeof(LayerRec) == 128, "layer record is 128 bytes");
 struct PrefillFused {
     const void* proj_weight;     // DN: [qkv; z; b; a] = 8224 x 1024, FA: [q; k; v] = 5120 x 1024
     const void* gate_up_weight;  // [gate; up] = 7168 x 1024
-    const void* unused[4];       // NVFP4 copies of the same matrices (not read by the BF16 path)
+    const void* proj_packed;     // optional NVFP4 (tensor-core layout) copies of the same two matrices: packed nibbles and scale atoms;
+    const void* proj_scales;     // DeltaNet projection rows padded to 8320.  When all four are set (and the caller did not switch it
+    const void* gate_up_packed;  // off) the two GEMMs run block-scaled on FP4 operands, activations quantised on the way
+    const void* gate_up_scales;  // (reference: prefill.cu:1210-1262, 1330-1347)
 };
 // Host copies of the two device tables, cached per pair of device addresses by the prefill launcher.
 struct HostTables { const void* dev_layers; const void* dev_fused; LayerRec layers[NUM_LAYERS]; PrefillFused fused[NUM_LAYERS]; };

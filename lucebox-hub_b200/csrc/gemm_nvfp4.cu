@@ -42,7 +42,7 @@ __host__ __device__ constexpr uint32_t fp4_stage_bytes(int t_tile) { return FP4_
 __host__ __device__ constexpr uint32_t fp4_smem(int t_tile) { return FP4_STAGES * fp4_stage_bytes(t_tile) + 1024 + 256; }
 
 struct Fp4GemmParams {
-    int T, N, K;                 // tokens, weight rows (output columns), reduction length
+    int T, N, K;                 // tokens, output columns (<= the weight rows the tensor map covers), reduction length
     void* C; int ldc;            // [T][ldc], bf16 (out_f32 = 0) or f32 (out_f32 = 1)
     const bf16* R; int ldr;      // optional residual, bf16 [T][ldr] (added after the rounding to bf16)
     const uint8_t* w_scales;     // atoms [N/128][K/64][512]
@@ -280,7 +280,7 @@ static int launch_fp4(const CUtensorMap& tmW, const CUtensorMap& tmA, const Fp4G
         Q35_CUDA_OK(cudaFuncSetAttribute(gemm_nvfp4_tcgen05_kernel<T_TILE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)fp4_smem(T_TILE)));
         attr.mark();
     }
-    const dim3 grid(p.N / FP4_BM, (p.T + T_TILE - 1) / T_TILE);
+    const dim3 grid((p.N + FP4_BM - 1) / FP4_BM, (p.T + T_TILE - 1) / T_TILE);
     if (g_pdl_launch) Q35_CUDA_OK(pdl_launch(gemm_nvfp4_tcgen05_kernel<T_TILE>, grid, dim3(FP4_THREADS), fp4_smem(T_TILE), stream, tmW, tmA, p));
     else gemm_nvfp4_tcgen05_kernel<T_TILE><<<grid, FP4_THREADS, fp4_smem(T_TILE), stream>>>(tmW, tmA, p);
     Q35_CUDA_OK(cudaGetLastError());
@@ -296,25 +296,26 @@ extern "C" size_t qwen35_b200_nvfp4_act_bytes(int tokens, int K, size_t* scales_
     return tpad * (size_t)(K / 2);
 }
 
-extern "C" int qwen35_b200_quantize_act_nvfp4(const void* x, int tokens, int K, void* packed_out, void* scales_out, qwen35_stream_t stream) {
-    using namespace q35;
+namespace q35 {
+
+int quantize_act_nvfp4(const bf16* x, int tokens, int K, void* packed_out, void* scales_out, cudaStream_t stream) {
     if (!x || !packed_out || !scales_out || tokens <= 0 || K <= 0 || K % 64 != 0) {
         set_error("quantize_act_nvfp4: tokens (%d) > 0 and K (%d) a multiple of 64 required", tokens, K);
         return QWEN35_ERR_BAD_ARG;
     }
     const long long tpad = ((long long)tokens + 127) / 128 * 128, nblk = tpad * (K / 16);
     const int blocks = (int)((nblk + 255) / 256 < 148 * 16 ? (nblk + 255) / 256 : 148 * 16);
-    Q35_CUDA_OK(pdl_launch(quantize_act_nvfp4_kernel, dim3(blocks), dim3(256), 0, (cudaStream_t)stream, (const bf16*)x, tokens, K, (uint8_t*)packed_out,
-                           (uint8_t*)scales_out, nblk));
+    Q35_CUDA_OK(pdl_launch(quantize_act_nvfp4_kernel, dim3(blocks), dim3(256), 0, stream, x, tokens, K, (uint8_t*)packed_out, (uint8_t*)scales_out, nblk));
     g_launches.fetch_add(1);
     return QWEN35_OK;
 }
 
-extern "C" int qwen35_b200_gemm_nvfp4(const void* a_packed, const void* a_scales, int tokens, const void* w_packed, const void* w_scales, int n_rows,
-                                      int K, float alpha, void* C, int ldc, int out_f32, const void* R, int ldr, qwen35_stream_t stream) {
-    using namespace q35;
-    if (!a_packed || !a_scales || !w_packed || !w_scales || !C || tokens <= 0 || n_rows <= 0 || n_rows % 128 != 0 || K <= 0 || K % 256 != 0) {
-        set_error("gemm_nvfp4: n_rows (%d) must be a multiple of 128 and K (%d) of 256, tokens (%d) > 0", n_rows, K, tokens);
+// n_rows: rows of the packed weight matrix (a multiple of 128: what the packer produced); n_out <= n_rows: output columns written
+int gemm_nvfp4(const void* a_packed, const void* a_scales, int tokens, const void* w_packed, const void* w_scales, int n_rows, int n_out, int K,
+               float alpha, void* C, int ldc, int out_f32, const bf16* R, int ldr, cudaStream_t stream) {
+    if (!a_packed || !a_scales || !w_packed || !w_scales || !C || tokens <= 0 || n_rows <= 0 || n_rows % 128 != 0 || n_out <= 0 || n_out > n_rows ||
+        K <= 0 || K % 256 != 0) {
+        set_error("gemm_nvfp4: n_rows (%d) must be a multiple of 128 and K (%d) of 256, tokens (%d) > 0, 0 < n_out (%d) <= n_rows", n_rows, K, tokens, n_out);
         return QWEN35_ERR_BAD_ARG;
     }
     int* err = (int*)get_workspace();
@@ -326,12 +327,22 @@ extern "C" int qwen35_b200_gemm_nvfp4(const void* a_packed, const void* a_scales
         set_error("gemm_nvfp4: tensor map creation failed (operands must be 16-byte aligned)");
         return QWEN35_ERR_CUDA;
     }
-    Fp4GemmParams p{tokens, n_rows, K, C, ldc, (const bf16*)R, ldr, (const uint8_t*)w_scales, (const uint8_t*)a_scales, alpha, out_f32, err};
-    cudaStream_t st = (cudaStream_t)stream;
+    Fp4GemmParams p{tokens, n_out, K, C, ldc, R, ldr, (const uint8_t*)w_scales, (const uint8_t*)a_scales, alpha, out_f32, err};
     switch (t_tile) {
-        case 16: return launch_fp4<16>(tmW, tmA, p, st);
-        case 32: return launch_fp4<32>(tmW, tmA, p, st);
-        case 64: return launch_fp4<64>(tmW, tmA, p, st);
-        default: return launch_fp4<128>(tmW, tmA, p, st);
+        case 16: return launch_fp4<16>(tmW, tmA, p, stream);
+        case 32: return launch_fp4<32>(tmW, tmA, p, stream);
+        case 64: return launch_fp4<64>(tmW, tmA, p, stream);
+        default: return launch_fp4<128>(tmW, tmA, p, stream);
     }
+}
+
+}  // namespace q35
+
+extern "C" int qwen35_b200_quantize_act_nvfp4(const void* x, int tokens, int K, void* packed_out, void* scales_out, qwen35_stream_t stream) {
+    return q35::quantize_act_nvfp4((const q35::bf16*)x, tokens, K, packed_out, scales_out, (cudaStream_t)stream);
+}
+
+extern "C" int qwen35_b200_gemm_nvfp4(const void* a_packed, const void* a_scales, int tokens, const void* w_packed, const void* w_scales, int n_rows,
+                                      int K, float alpha, void* C, int ldc, int out_f32, const void* R, int ldr, qwen35_stream_t stream) {
+    return q35::gemm_nvfp4(a_packed, a_scales, tokens, w_packed, w_scales, n_rows, n_rows, K, alpha, C, ldc, out_f32, (const q35::bf16*)R, ldr, (cudaStream_t)stream);
 }

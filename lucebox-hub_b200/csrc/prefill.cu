@@ -19,6 +19,9 @@ namespace q35 {
 
 int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ldc, const bf16* R, int ldr,
               int M, int N, int K, int epi, int up_row_offset, cudaStream_t stream);
+int quantize_act_nvfp4(const bf16* x, int tokens, int K, void* packed_out, void* scales_out, cudaStream_t stream);
+int gemm_nvfp4(const void* a_packed, const void* a_scales, int tokens, const void* w_packed, const void* w_scales, int n_rows, int n_out, int K,
+               float alpha, void* C, int ldc, int out_f32, const bf16* R, int ldr, cudaStream_t stream);
 
 // grow-only per-device scratch for the chunk-local results
 static void* g_scratch[64] = {};
@@ -72,8 +75,17 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
         attr_done.mark();
     }
     const int nchunks = (S + DN_CHUNK - 1) / DN_CHUNK;
-    ChunkScratch* scratch = (ChunkScratch*)get_scratch((size_t)DN_HEADS * nchunks * sizeof(ChunkScratch));
-    if (!scratch) return QWEN35_ERR_CUDA;
+    // library scratch: the chunk-local results, then the NVFP4 operand of the activations (packed rows padded to 128 + scale
+    // atoms) and one row of bf16 logits for the tensor-core FP4 head
+    const size_t chunk_bytes = ((size_t)DN_HEADS * nchunks * sizeof(ChunkScratch) + 255) & ~(size_t)255;
+    const size_t tpad = ((size_t)S + 127) / 128 * 128;
+    const size_t act_packed_bytes = tpad * (HIDDEN / 2), act_scale_bytes = tpad / 128 * (HIDDEN / 64) * 512;
+    char* scratch_base = (char*)get_scratch(chunk_bytes + act_packed_bytes + act_scale_bytes + (size_t)VOCAB * 2 + 256);
+    if (!scratch_base) return QWEN35_ERR_CUDA;
+    ChunkScratch* scratch = (ChunkScratch*)scratch_base;
+    uint8_t* act_packed = (uint8_t*)scratch_base + chunk_bytes;
+    uint8_t* act_scales = act_packed + act_packed_bytes;
+    bf16* lm_logits = (bf16*)(act_scales + ((act_scale_bytes + 255) & ~(size_t)255));
     RopeTable rt;
     for (int i = 0; i < FA_ROT / 2; ++i) rt.f[i] = 1.0f / (float)std::pow(1.0e7, (double)((float)(2 * i) / (float)FA_ROT));
 
@@ -85,6 +97,9 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
         // Without fused tables (launch_prefill_bf16_mega) every matrix of the layer record is its own GEMM, written into the
         // same column blocks of proj_buf the fused projection fills, and SiLU * up is a kernel of its own.
         const PrefillFused* F = a.fused_host ? &a.fused_host[layer] : nullptr;
+        // NVFP4 copies of the two fused matrices present: their GEMMs run block-scaled on FP4 operands (activations quantised
+        // per 16-element block on the way), as the reference does when its table carries them (prefill.cu:1210-1218)
+        const bool fp4 = F && F->proj_packed && F->proj_scales && F->gate_up_packed && F->gate_up_scales;
         // input norm (layer 0 gathers the embedding rows into `hidden` on the way); with a teacher, layer l > 0 takes its
         // input (and the residual of its mixer) from the teacher's row block instead of the previous layer's output
         const bf16* layer_in = (a.dbg_teacher && layer > 0) ? a.dbg_teacher + (size_t)layer * S * HIDDEN : a.hidden;
@@ -94,7 +109,11 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
         const bf16 *w_out, *w_post, *w_down;
         if (L.type == 0) {
             const int ldp = DN_PROJ_ROWS;
-            if (F) {
+            if (fp4) {
+                Q35_TRY(quantize_act_nvfp4(a.normalized, S, HIDDEN, act_packed, act_scales, stream));
+                Q35_TRY(gemm_nvfp4(act_packed, act_scales, S, F->proj_packed, F->proj_scales, (DN_PROJ_ROWS + 127) / 128 * 128, DN_PROJ_ROWS, HIDDEN, 1.0f,
+                                   a.proj_buf, ldp, 0, nullptr, 0, stream));
+            } else if (F) {
                 Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)F->proj_weight, DN_PROJ_ROWS, a.proj_buf, ldp, nullptr, 0, S, DN_PROJ_ROWS, HIDDEN, 0, 0, stream));
             } else {
                 const int slot[4] = {DN_QKV, DN_Z, DN_B, DN_A}, rows[4] = {DN_CONV_CH, DN_V_SIZE, DN_HEADS, DN_HEADS};
@@ -113,7 +132,11 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
             ++i_dn;
         } else {
             const int ldp = FA_PROJ_ROWS;
-            if (F) {
+            if (fp4) {
+                Q35_TRY(quantize_act_nvfp4(a.normalized, S, HIDDEN, act_packed, act_scales, stream));
+                Q35_TRY(gemm_nvfp4(act_packed, act_scales, S, F->proj_packed, F->proj_scales, FA_PROJ_ROWS, FA_PROJ_ROWS, HIDDEN, 1.0f, a.proj_buf, ldp, 0,
+                                   nullptr, 0, stream));
+            } else if (F) {
                 Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)F->proj_weight, FA_PROJ_ROWS, a.proj_buf, ldp, nullptr, 0, S, FA_PROJ_ROWS, HIDDEN, 0, 0, stream));
             } else {
                 const int slot[3] = {FA_Q, FA_K, FA_V}, rows[3] = {FA_QPROJ, FA_KV_SIZE, FA_KV_SIZE};
@@ -134,7 +157,14 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
         Q35_TRY(gemm_bf16(a.attn_buf, 2048, w_out, HIDDEN, a.residual, HIDDEN, layer_in, HIDDEN, S, HIDDEN, 2048, 1, 0, stream));
         Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, S, 128, 0, stream, nullptr, nullptr, a.residual, w_post, nullptr, a.normalized, S));
         g_launches.fetch_add(1);
-        if (F) {
+        if (fp4) {
+            // [gate | up] rows of one block-scaled GEMM into proj_buf ([S, 7168]; the projection buffer is free again), then SiLU * up
+            Q35_TRY(quantize_act_nvfp4(a.normalized, S, HIDDEN, act_packed, act_scales, stream));
+            Q35_TRY(gemm_nvfp4(act_packed, act_scales, S, F->gate_up_packed, F->gate_up_scales, 2 * INTER, 2 * INTER, HIDDEN, 1.0f, a.proj_buf, 2 * INTER, 0,
+                               nullptr, 0, stream));
+            Q35_CUDA_OK(pdl_launch(pf_silu_mul_rows_kernel, (S * (INTER / 8) + 255) / 256, 256, 0, stream, (const bf16*)a.proj_buf, a.mlp_buf, S));
+            g_launches.fetch_add(1);
+        } else if (F) {
             Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)F->gate_up_weight, 2 * INTER, a.mlp_buf, INTER, nullptr, 0, S, INTER, HIDDEN, 2, INTER, stream));
         } else {
             // the projection buffers are free again here: gate -> proj_buf, up -> proj_buf2 (both [S, 3584])
@@ -154,12 +184,18 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
     if (a.hidden_out) Q35_CUDA_OK(cudaMemcpyAsync(a.hidden_out, last, HIDDEN * sizeof(bf16), cudaMemcpyDeviceToDevice, stream));
     Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, 1, 128, 0, stream, nullptr, nullptr, last, a.final_norm, nullptr, a.final_normed, 1));
     const int lm_blocks = 592;
-    if (a.lm_packed)
-        Q35_CUDA_OK(pdl_launch(pf_lm_head_fp4_kernel, lm_blocks, 256, 0, stream, a.final_normed, (const uint8_t*)a.lm_packed, (const uint8_t*)a.lm_scales, a.lm_bmv, a.lm_bmi, a.logits_out));
-    else
+    if (a.lm_packed) {
+        // the reference's FP4 head (kernel_gb10_nvfp4.cu:1945-1997): the normed hidden row is quantised to NVFP4 as well and the
+        // block-scaled tensor-core GEMM gives the logits, rounded once to bf16; arg-max with the lowest index among ties
+        Q35_TRY(quantize_act_nvfp4(a.final_normed, 1, HIDDEN, act_packed, act_scales, stream));
+        Q35_TRY(gemm_nvfp4(act_packed, act_scales, 1, a.lm_packed, a.lm_scales, VOCAB, VOCAB, HIDDEN, 1.0f, lm_logits, VOCAB, 0, nullptr, 0, stream));
+        Q35_CUDA_OK(pdl_launch(pf_argmax_row_kernel, 1, 1024, 0, stream, (const bf16*)lm_logits, a.out_token, a.logits_out));
+        g_launches.fetch_add(2);
+    } else {
         Q35_CUDA_OK(pdl_launch(pf_lm_head_kernel, lm_blocks, 256, 0, stream, a.final_normed, a.lm_head, a.lm_bmv, a.lm_bmi, a.logits_out));
-    Q35_CUDA_OK(pdl_launch(pf_lm_reduce_kernel, 1, 32, 0, stream, a.lm_bmv, a.lm_bmi, lm_blocks, a.out_token));
-    g_launches.fetch_add(3);
+        Q35_CUDA_OK(pdl_launch(pf_lm_reduce_kernel, 1, 32, 0, stream, a.lm_bmv, a.lm_bmi, lm_blocks, a.out_token));
+        g_launches.fetch_add(3);
+    }
     Q35_CUDA_OK(cudaGetLastError());
     return QWEN35_OK;
 }

@@ -70,6 +70,54 @@ static __global__ void __launch_bounds__(256) pf_silu_mul_kernel(const bf16* __r
     reinterpret_cast<uint4*>(out)[i] = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// the same over one [S, 2 * INTER] buffer whose rows hold [gate | up] (output of the fused NVFP4 gate/up GEMM)
+static __global__ void __launch_bounds__(256) pf_silu_mul_rows_kernel(const bf16* __restrict__ gu, bf16* __restrict__ out, int S) {
+    pdl_wait();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= S * (INTER / 8)) return;
+    const int t = i / (INTER / 8), c = i % (INTER / 8);
+    const uint4 g = reinterpret_cast<const uint4*>(gu + (size_t)t * 2 * INTER)[c], u = reinterpret_cast<const uint4*>(gu + (size_t)t * 2 * INTER + INTER)[c];
+    const uint32_t gw[4] = {g.x, g.y, g.z, g.w}, uw[4] = {u.x, u.y, u.z, u.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const __nv_bfloat162 pr = __halves2bfloat162(f2bf(rbf(silu_f(bf_lo(gw[j]))) * bf_lo(uw[j])), f2bf(rbf(silu_f(bf_hi(gw[j]))) * bf_hi(uw[j])));
+        o[j] = *reinterpret_cast<const uint32_t*>(&pr);
+    }
+    reinterpret_cast<uint4*>(out + (size_t)t * INTER)[c] = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// arg-max over one row of bf16 logits (lowest index among equal maxima), optional f32 copy of the row; one CTA of 1024 threads
+static __global__ void __launch_bounds__(1024) pf_argmax_row_kernel(const bf16* __restrict__ logits, int* __restrict__ out_token, float* __restrict__ logits_out) {
+    pdl_wait();
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const int tid = threadIdx.x;
+    float best = -INFINITY;
+    int best_i = 0x7fffffff;
+    for (int c = tid; c < VOCAB; c += 1024) {
+        const float f = bf2f(logits[c]);
+        if (logits_out) logits_out[c] = f;
+        if (f > best) { best = f; best_i = c; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float v = __shfl_xor_sync(0xffffffffu, best, o); const int k = __shfl_xor_sync(0xffffffffu, best_i, o);
+        if (v > best || (v == best && k < best_i)) { best = v; best_i = k; }
+    }
+    if ((tid & 31) == 0) { sv[tid >> 5] = best; si[tid >> 5] = best_i; }
+    __syncthreads();
+    if (tid < 32) {
+        best = sv[tid]; best_i = si[tid];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float v = __shfl_xor_sync(0xffffffffu, best, o); const int k = __shfl_xor_sync(0xffffffffu, best_i, o);
+            if (v > best || (v == best && k < best_i)) { best = v; best_i = k; }
+        }
+        if (tid == 0 && out_token) *out_token = best_i;
+    }
+}
+
 // ---- DeltaNet preparation: one CTA (128 threads) per (token, head) -----------------------------------
 // proj: [S, ldp] bf16 rows [qkv 6144 | z 2048 | b 16 | a 16].  Writes qkv_out [S, 6144] bf16 (q, k L2-normalised
 // in bf16 arithmetic, v after conv + SiLU), beta [S,16] (bf16-rounded sigmoid), g [S,16] (f32 log-decay).
@@ -797,55 +845,6 @@ static __global__ void __launch_bounds__(256) pf_lm_head_kernel(const bf16* __re
     if (threadIdx.x == 0) {
         float bv = sv[0]; int bi = si[0];
         for (int w = 1; w < 8; ++w) if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
-        bmv[blockIdx.x] = bv; bmi[blockIdx.x] = bi;
-    }
-}
-
-// NVFP4 LM head (tensor-core layout: packed E2M1 [V,512], E4M3 block scales in 128x4 swizzled tiles), one warp per row.
-// Reference: lm_head_kernel_nvfp4 (kernel_gb10_nvfp4.cu:1451-1523), the path its hybrid prefill ends with.
-static __global__ void __launch_bounds__(256) pf_lm_head_fp4_kernel(const bf16* __restrict__ x, const uint8_t* __restrict__ packed,
-                                                             const uint8_t* __restrict__ scales, float* __restrict__ bmv, int* __restrict__ bmi,
-                                                             float* __restrict__ logits_out) {
-    pdl_wait();
-    __shared__ float sv[8];
-    __shared__ int si[8];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float xr[32];                                  // elements [32 lane, 32 lane + 32)
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const uint4 v = *(reinterpret_cast<const uint4*>(x + 32 * lane) + j);
-        xr[8 * j + 0] = bf_lo(v.x); xr[8 * j + 1] = bf_hi(v.x); xr[8 * j + 2] = bf_lo(v.y); xr[8 * j + 3] = bf_hi(v.y);
-        xr[8 * j + 4] = bf_lo(v.z); xr[8 * j + 5] = bf_hi(v.z); xr[8 * j + 6] = bf_lo(v.w); xr[8 * j + 7] = bf_hi(v.w);
-    }
-    const int r0 = part_begin(VOCAB, blockIdx.x, gridDim.x), r1 = part_begin(VOCAB, blockIdx.x + 1, gridDim.x);
-    float best = -INFINITY;
-    int best_i = 0x7fffffff;
-    for (int r = r0 + warp; r < r1; r += 8) {
-        const uint4 pk = ld_stream(reinterpret_cast<const uint4*>(packed + (size_t)r * (HIDDEN / 2)) + lane);
-        const size_t tile = (size_t)(r >> 7) * (HIDDEN / 64) + (lane >> 1);
-        const unsigned short sraw = __ldg(reinterpret_cast<const unsigned short*>(scales + tile * 512 + (r & 31) * 16 + ((r & 127) >> 5) * 4 + ((2 * lane) & 3)));
-        const __half2_raw sh = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)sraw, __NV_E4M3);
-        const float2 sc = __half22float2(*reinterpret_cast<const __half2*>(&sh));
-        const uint32_t w[4] = {pk.x, pk.y, pk.z, pk.w};
-        float a[2] = {0.f, 0.f};
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int bb = 0; bb < 4; ++bb) {
-                const __half2_raw h = __nv_cvt_fp4x2_to_halfraw2((__nv_fp4x2_storage_t)((w[i] >> (8 * bb)) & 0xffu), __NV_E2M1);
-                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
-                a[i >> 1] = fmaf(f.x, xr[i * 8 + bb * 2], a[i >> 1]);
-                a[i >> 1] = fmaf(f.y, xr[i * 8 + bb * 2 + 1], a[i >> 1]);
-            }
-        const float v = rbf(warp_sum(a[0] * sc.x + a[1] * sc.y));
-        if (lane == 0 && logits_out) logits_out[r] = v;
-        if (v > best) { best = v; best_i = r; }
-    }
-    if (lane == 0) { sv[warp] = best; si[warp] = best_i; }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float bv = sv[0]; int bi = si[0];
-        for (int w2 = 1; w2 < 8; ++w2) if (sv[w2] > bv || (sv[w2] == bv && si[w2] < bi)) { bv = sv[w2]; bi = si[w2]; }
         bmv[blockIdx.x] = bv; bmi[blockIdx.x] = bi;
     }
 }

@@ -184,12 +184,32 @@ def _attach_prefill_fused_weights(weights):
     weights["prefill_fused_layer_data"] = fused
 
 
-def _pack_prefill_fused_layer_weights(fused_layer_data, device="cuda"):
-    """Device blob of 6-pointer records (reference model.py:450-470); the four NVFP4 slots stay null."""
+def _attach_prefill_nvfp4_weights(weights, verbose=False):
+    """NVFP4 (tensor-core layout) copies of the two fused prompt matrices of every layer (reference model.py:190-215): the
+    DeltaNet projection padded to 8320 rows, gate/up as it is.  With them in the fused table the prompt pass runs those two
+    GEMMs block-scaled on FP4 operands."""
+    _attach_prefill_fused_weights(weights)
+    fused = weights["prefill_fused_layer_data"]
+    if fused and "proj_weight_packed" in fused[0]:
+        return weights
+    for ld, f in zip(weights["layer_data"], fused):
+        rows = DN_PROJ_FUSED_PADDED_SIZE if ld["type"] == 0 else f["proj_weight"].shape[0]
+        pq = _quantize_matrix_nvfp4_tc(f["proj_weight"], padded_rows=rows)
+        gq = _quantize_matrix_nvfp4_tc(f["gate_up_weight"])
+        f["proj_weight_packed"], f["proj_weight_scales"] = pq["packed"], pq["scales"]
+        f["gate_up_weight_packed"], f["gate_up_weight_scales"] = gq["packed"], gq["scales"]
+    return weights
+
+
+def _pack_prefill_fused_layer_weights(fused_layer_data, device="cuda", with_nvfp4=True):
+    """Device blob of 6-pointer records (reference model.py:450-470): bf16 projection and gate/up, then the packed / scales
+    pairs of their NVFP4 copies (null when the weights carry none, or with_nvfp4=False)."""
     _capi.lib().qwen35_b200_forget_tables()       # a new table may reuse the address of a freed one
     buf = bytearray(len(fused_layer_data) * 48)
     for i, ld in enumerate(fused_layer_data):
-        struct.pack_into("QQQQQQ", buf, i * 48, ld["proj_weight"].data_ptr(), ld["gate_up_weight"].data_ptr(), 0, 0, 0, 0)
+        q = [ld[k].data_ptr() if (with_nvfp4 and k in ld) else 0
+             for k in ("proj_weight_packed", "proj_weight_scales", "gate_up_weight_packed", "gate_up_weight_scales")]
+        struct.pack_into("QQQQQQ", buf, i * 48, ld["proj_weight"].data_ptr(), ld["gate_up_weight"].data_ptr(), *q)
     return torch.frombuffer(buf, dtype=torch.uint8).to(device)
 
 
@@ -214,7 +234,9 @@ class Decoder:
     """Stateful greedy decoder, batch 1 (reference: model.py:473)."""
 
     def __init__(self, weights=None, tokenizer=None, model_name="random:1234", backend="bf16",
-                 verbose=False, max_seq_len=MAX_SEQ_LEN, device="cuda"):
+                 verbose=False, max_seq_len=MAX_SEQ_LEN, device="cuda", prefill_nvfp4=False):
+        """prefill_nvfp4=True: the batched prompt pass runs its fused projection and gate/up GEMMs and the LM head block-scaled
+        on NVFP4 operands (the reference's tensor-core prompt option, prefill.cu:1210-1262 + prefill_bf16_nvfp4_lm)."""
         if backend not in ("bf16", "nvfp4", "auto", None):
             raise ValueError(f"unsupported backend: {backend}")
         self.backend = "nvfp4" if backend == "nvfp4" else "bf16"
@@ -232,8 +254,15 @@ class Decoder:
         self._final_norm_weight = weights["final_norm_weight"]
         self._lm_head_weight = weights["lm_head_weight"]
         self._layer_weights_packed = _pack_layer_weights(weights["layer_data"], device)
-        _attach_prefill_fused_weights(weights)
-        self._prefill_fused_weights_packed = _pack_prefill_fused_layer_weights(weights["prefill_fused_layer_data"], device)
+        self.prefill_nvfp4 = bool(prefill_nvfp4)
+        if self.prefill_nvfp4:
+            _attach_prefill_nvfp4_weights(weights)
+            if "prefill_lm_nvfp4" not in weights:
+                weights["prefill_lm_nvfp4"] = _quantize_matrix_nvfp4_lm(weights["lm_head_weight"])
+            self._prefill_lm_packed, self._prefill_lm_scales = weights["prefill_lm_nvfp4"]["packed"], weights["prefill_lm_nvfp4"]["scales"]
+        else:
+            _attach_prefill_fused_weights(weights)
+        self._prefill_fused_weights_packed = _pack_prefill_fused_layer_weights(weights["prefill_fused_layer_data"], device, with_nvfp4=self.prefill_nvfp4)
         self._prefill_buffers = None
         self._prefill_buffer_tokens = 0
         self._layer_weights_packed_nvfp4 = None
@@ -381,6 +410,8 @@ class Decoder:
                 setattr(a, k, b[k].data_ptr())
             a.logits_out = _capi.ptr(logits_out); a.max_seq_len = self.max_seq_len; a.dbg_num_layers = dbg_num_layers
             a.dbg_teacher = _capi.ptr(dbg_teacher); a.dbg_hidden = _capi.ptr(dbg_hidden)
+            if self.prefill_nvfp4 and mode != "mega":
+                a.lm_head_weight_packed = self._prefill_lm_packed.data_ptr(); a.lm_head_scales = self._prefill_lm_scales.data_ptr()
             with torch.cuda.device(self.device):
                 _capi.check(self._lib.qwen35_b200_prefill_bf16(C.byref(a), self._stream()), "prefill_bf16")
             self._hidden.copy_(b["hidden_bf16_out"])
@@ -459,7 +490,7 @@ class BatchedDecoder:
         self._weights = weights
         _attach_prefill_fused_weights(weights)
         self._layer_weights_packed = _pack_layer_weights(weights["layer_data"], device)
-        self._prefill_fused_weights_packed = _pack_prefill_fused_layer_weights(weights["prefill_fused_layer_data"], device)
+        self._prefill_fused_weights_packed = _pack_prefill_fused_layer_weights(weights["prefill_fused_layer_data"], device, with_nvfp4=False)
         # host copies of the two tables: with them a step never synchronises
         self._graph = None; self._warm = False
         self._layer_weights_host = self._layer_weights_packed.cpu()

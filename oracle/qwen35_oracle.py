@@ -50,12 +50,39 @@ def f64_to_bf16_once(x: torch.Tensor) -> torch.Tensor:
     return bits.view(torch.float32).to(torch.bfloat16)
 
 
+NVFP4_LINEAR = None       # optional {id(weight): dequantised f32 copy}: those projections are taken on NVFP4 operands (below)
+
+
+def fake_quant_nvfp4_rows(x: torch.Tensor) -> torch.Tensor:
+    """The values a row-major activation matrix has after quantisation to NVFP4 in the tensor-core layout
+    (16-element blocks along K, UE4M3 scale = sat_rn(max(amax/6, 2^-28)), elements divided by the decoded scale and rounded
+    to E2M1 to nearest even; the reference quantises prompt activations this way, prefill.cu:1210-1262 with the kernel of
+    kernel_gb10_nvfp4.cu:1366-1430), as f32."""
+    import numpy as np
+    from . import nvfp4_ref as nv
+    a = x.float().numpy().astype(np.float32)
+    rows, cols = a.shape
+    g = a.reshape(rows, cols // 16, 16)
+    amax = np.abs(g).max(axis=-1)
+    scale_f = np.maximum(amax * np.float32(1.0 / 6.0), np.float32(2.0 ** -28)).astype(np.float32)
+    dec = nv.e4m3_decode(nv.e4m3_encode(scale_f))
+    with np.errstate(divide="ignore"):
+        inv = np.where(dec > 0, np.float32(1.0) / dec, np.float32(0.0)).astype(np.float32)
+    codes = nv.e2m1_rne((g * inv[..., None]).astype(np.float32))
+    vals = nv.E2M1_VALUES[codes & 7] * np.where(codes & 8, np.float32(-1.0), np.float32(1.0))
+    return torch.from_numpy((vals * dec[..., None]).astype(np.float32).reshape(rows, cols))
+
+
 def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """Projection with f32 accumulation and one rounding to the activation dtype.  bf16 weights go through
     F.linear (what a bf16 HuggingFace model does).  f32 weights are used for the NVFP4 variant, whose dequantised
     values (E2M1 code x fp16 or E4M3 scale) are exact in f32 but not in bf16 (kernel_gb10_nvfp4.cu:521-545).
     With EXACT_LINEAR the sum is taken in f64 (products of bf16 values are exact there and a 3584-term sum loses
     nothing that matters at 2^-53) and rounded once: the value every f32 summation order approximates."""
+    if NVFP4_LINEAR is not None and id(w) in NVFP4_LINEAR:
+        # block-scaled FP4 GEMM: both operands on the E2M1 x E4M3 grid, products and sums exact in f64, one rounding
+        xq = fake_quant_nvfp4_rows(x.reshape(-1, x.shape[-1]))
+        return f64_to_bf16_once(F.linear(xq.double(), NVFP4_LINEAR[id(w)].double())).reshape(*x.shape[:-1], -1).to(x.dtype)
     if EXACT_LINEAR and x.dtype == torch.bfloat16:
         return f64_to_bf16_once(F.linear(x.double(), w.double()))
     if w.dtype == x.dtype:

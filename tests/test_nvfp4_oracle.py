@@ -92,3 +92,28 @@ def test_random_matrix_error_bound():
     for deq in (R.dequantize_nvfp4_lm(*R.quantize_nvfp4_lm(w)), R.dequantize_nvfp4(*R.quantize_nvfp4(w, 32), 32)):
         err = np.abs(deq - w)
         assert err.max() < 0.02 and err.mean() < 0.003
+
+
+def test_activation_fake_quant_equals_pack_then_unpack():
+    """The oracle's NVFP4 view of an activation matrix (used for the FP4 prompt GEMMs) is the tensor-core packer followed
+    by its dequantiser, and a projection registered in NVFP4_LINEAR is the exact product of the two dequantised operands."""
+    import torch
+    import oracle.qwen35_oracle as om
+    from oracle.nvfp4_ref import dequantize_nvfp4_lm, quantize_nvfp4_lm
+    torch.manual_seed(5)
+    x = (torch.randn(128, 256) * 3).bfloat16()
+    x[7] = 0
+    fq = om.fake_quant_nvfp4_rows(x)
+    ref = dequantize_nvfp4_lm(*quantize_nvfp4_lm(x.float().numpy()))
+    assert np.array_equal(fq.numpy(), ref)
+    w = (torch.randn(128, 256) * 0.1).bfloat16()
+    wq = torch.from_numpy(dequantize_nvfp4_lm(*quantize_nvfp4_lm(w.float().numpy())))
+    om.NVFP4_LINEAR = {id(w): wq}
+    try:
+        y = om.linear(x, w)
+        y_plain = om.linear(x, w.clone())
+    finally:
+        om.NVFP4_LINEAR = None
+    want = (fq.double() @ wq.double().t())
+    assert y.dtype == torch.bfloat16 and float((y.double() - want).abs().max()) <= float(want.abs().max()) * 2.0 ** -8
+    assert not torch.equal(y, y_plain)
