@@ -72,6 +72,7 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
         Q35_CUDA_OK(cudaFuncSetAttribute(pf_dn_chunk_local_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CHUNK_LOCAL_SMEM));
         Q35_CUDA_OK(cudaFuncSetAttribute(pf_dn_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CHUNK_SCAN_SMEM));
         Q35_CUDA_OK(cudaFuncSetAttribute(pf_attention_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_MMA_SMEM));
+        Q35_CUDA_OK(cudaFuncSetAttribute(pf_attention_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ATS_SMEM));
         attr_done.mark();
     }
     const int nchunks = (S + DN_CHUNK - 1) / DN_CHUNK;
@@ -120,7 +121,7 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
                 for (int i = 0, col = 0; i < 4; col += rows[i], ++i)
                     Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)L.p[slot[i]], rows[i], a.proj_buf + col, ldp, nullptr, 0, S, rows[i], HIDDEN, 0, 0, stream));
             }
-            Q35_CUDA_OK(pdl_launch(pf_dn_prep_kernel, dim3(S, DN_HEADS), 128, 0, stream, a.proj_buf, ldp, (const bf16*)L.p[DN_CONV], (const bf16*)L.p[DN_ALOG],
+            Q35_CUDA_OK(pdl_launch(pf_dn_prep_kernel, (S * DN_HEADS + DN_PREP_WARPS - 1) / DN_PREP_WARPS, 32 * DN_PREP_WARPS, 0, stream, a.proj_buf, ldp, (const bf16*)L.p[DN_CONV], (const bf16*)L.p[DN_ALOG],
                                                                       (const bf16*)L.p[DN_DTBIAS], a.proj_buf2, a.beta_buf, a.alpha_buf, S));
             Q35_CUDA_OK(pdl_launch(pf_conv_state_kernel, (DN_CONV_CH + 255) / 256, 256, 0, stream, a.proj_buf, ldp, a.conv_bufs + (size_t)i_dn * DN_CONV_CH * 4, S));
             Q35_CUDA_OK(pdl_launch(pf_dn_chunk_local_kernel, dim3(nchunks, DN_HEADS), CL_THREADS, CHUNK_LOCAL_SMEM, stream, a.proj_buf2, a.beta_buf, a.alpha_buf, scratch, S, nchunks));
@@ -147,8 +148,12 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
             bf16* vc = a.v_cache + (size_t)i_fa * FA_KV_HEADS * a.max_seq_len * FA_HEAD_DIM;
             Q35_CUDA_OK(pdl_launch(pf_qk_norm_rope_kernel, (S * 12 + 7) / 8, 256, 0, stream, a.proj_buf, ldp, (const bf16*)L.p[FA_QNORM], (const bf16*)L.p[FA_KNORM], rt,
                                                                          a.proj_buf2, kc, vc, S, a.max_seq_len));
-            Q35_CUDA_OK(pdl_launch(pf_attention_mma_kernel, dim3((S + ATT_MMA_Q - 1) / ATT_MMA_Q, FA_KV_HEADS), 256, ATT_MMA_SMEM, stream, 
-                a.proj_buf2, kc, vc, a.proj_buf, ldp, a.attn_buf, S, a.max_seq_len));
+            if (S <= ATS_MAX_S)
+                Q35_CUDA_OK(pdl_launch(pf_attention_split_kernel, dim3((S + ATS_Q - 1) / ATS_Q, FA_KV_HEADS), 256, ATS_SMEM, stream,
+                    a.proj_buf2, kc, vc, a.proj_buf, ldp, a.attn_buf, S, a.max_seq_len));
+            else
+                Q35_CUDA_OK(pdl_launch(pf_attention_mma_kernel, dim3((S + ATT_MMA_Q - 1) / ATT_MMA_Q, FA_KV_HEADS), 256, ATT_MMA_SMEM, stream,
+                    a.proj_buf2, kc, vc, a.proj_buf, ldp, a.attn_buf, S, a.max_seq_len));
             g_launches.fetch_add(2);
             w_out = (const bf16*)L.p[FA_O]; w_post = (const bf16*)L.p[FA_POST_NORM]; w_down = (const bf16*)L.p[FA_DOWN];
             ++i_fa;

@@ -118,51 +118,62 @@ static __global__ void __launch_bounds__(1024) pf_argmax_row_kernel(const bf16* 
     }
 }
 
-// ---- DeltaNet preparation: one CTA (128 threads) per (token, head) -----------------------------------
+// ---- DeltaNet preparation: one warp per (token, head), a lane takes four adjacent dimensions of q, k and v ------------
 // proj: [S, ldp] bf16 rows [qkv 6144 | z 2048 | b 16 | a 16].  Writes qkv_out [S, 6144] bf16 (q, k L2-normalised
 // in bf16 arithmetic, v after conv + SiLU), beta [S,16] (bf16-rounded sigmoid), g [S,16] (f32 log-decay).
-static __global__ void __launch_bounds__(128) pf_dn_prep_kernel(const bf16* __restrict__ proj, int ldp, const bf16* __restrict__ conv_w,
+constexpr int DN_PREP_WARPS = 8;
+static __global__ void __launch_bounds__(32 * DN_PREP_WARPS) pf_dn_prep_kernel(const bf16* __restrict__ proj, int ldp, const bf16* __restrict__ conv_w,
                                                          const bf16* __restrict__ a_log, const bf16* __restrict__ dt_bias,
                                                          bf16* __restrict__ qkv_out, float* __restrict__ beta, float* __restrict__ g, int S) {
     pdl_wait();
-    __shared__ float red[2][4];
-    const int t = blockIdx.x, h = blockIdx.y, i = threadIdx.x;
-    float c[3];
+    const int unit = blockIdx.x * DN_PREP_WARPS + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (unit >= S * DN_HEADS) return;
+    const int t = unit / DN_HEADS, h = unit % DN_HEADS;
+    float c[3][4];
 #pragma unroll
     for (int part = 0; part < 3; ++part) {
-        const int ch = part * DN_QK_SIZE + h * DN_K + i;
-        const uint2 wr = __ldg(reinterpret_cast<const uint2*>(conv_w) + ch);
-        const float w4[4] = {bf_lo(wr.x), bf_hi(wr.x), bf_lo(wr.y), bf_hi(wr.y)};
-        float acc = 0.f;
-        bool first = true;
+        const int ch = part * DN_QK_SIZE + h * DN_K + 4 * lane;
+        const uint4 w01 = __ldg(reinterpret_cast<const uint4*>(conv_w + (size_t)ch * 4));         // taps of channels ch, ch + 1
+        const uint4 w23 = __ldg(reinterpret_cast<const uint4*>(conv_w + (size_t)ch * 4) + 1);     // ch + 2, ch + 3
+        const uint32_t wr[8] = {w01.x, w01.y, w01.z, w01.w, w23.x, w23.y, w23.z, w23.w};
+        uint2 xr[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int tt = t - 3 + j;
-            const float xv = (tt >= 0) ? bf2f(proj[(size_t)tt * ldp + ch]) : 0.f;
-            acc = first ? w4[j] * xv : fmaf(w4[j], xv, acc);
-            first = false;
+            xr[j] = (tt >= 0) ? *reinterpret_cast<const uint2*>(proj + (size_t)tt * ldp + ch) : make_uint2(0u, 0u);
         }
-        c[part] = rbf(silu_f(rbf(acc)));
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float w4[4] = {bf_lo(wr[2 * e]), bf_hi(wr[2 * e]), bf_lo(wr[2 * e + 1]), bf_hi(wr[2 * e + 1])};
+            float acc = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t pair = (e < 2) ? xr[j].x : xr[j].y;
+                const float xv = (e & 1) ? bf_hi(pair) : bf_lo(pair);
+                acc = (j == 0) ? w4[j] * xv : fmaf(w4[j], xv, acc);
+            }
+            c[part][e] = rbf(silu_f(rbf(acc)));
+        }
     }
     // L2 norm of q and k in bf16 arithmetic: squares rounded, f32 sum rounded once, + eps, rsqrt, scale.
-    const float sq0 = warp_sum(rbf(c[0] * c[0])), sq1 = warp_sum(rbf(c[1] * c[1]));
-    if ((i & 31) == 0) { red[0][i >> 5] = sq0; red[1][i >> 5] = sq1; }
-    __syncthreads();
     // torch's vectorised CPU rsqrt rounds once; its scalar tail (the last S*16 mod 32 elements, i.e. the last
     // token when S is odd) rounds sqrt to bf16 first.  The oracle is that CPU path, so both are mirrored.
     const bool scalar_tail = (S & 1) && (t == S - 1);
 #pragma unroll
     for (int part = 0; part < 2; ++part) {
-        float tot = ((red[part][0] + red[part][1]) + red[part][2]) + red[part][3];
+        float tot = warp_sum(((rbf(c[part][0] * c[part][0]) + rbf(c[part][1] * c[part][1])) + rbf(c[part][2] * c[part][2])) + rbf(c[part][3] * c[part][3]));
         tot = rbf(rbf(tot) + 1e-6f);
         const float inv = scalar_tail ? rbf(1.0f / rbf(sqrtf(tot))) : rbf(rsqrt_ieee(tot));
-        c[part] = rbf(c[part] * inv);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) c[part][e] = rbf(c[part][e] * inv);
     }
-    bf16* dst = qkv_out + (size_t)t * DN_CONV_CH + h * DN_K + i;
-    dst[0] = f2bf(c[0]);
-    dst[DN_QK_SIZE] = f2bf(c[1]);
-    dst[2 * DN_QK_SIZE] = f2bf(c[2]);
-    if (i == 0) {
+    bf16* dst = qkv_out + (size_t)t * DN_CONV_CH + h * DN_K + 4 * lane;
+#pragma unroll
+    for (int part = 0; part < 3; ++part) {
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(c[part][0], c[part][1]), hi = __floats2bfloat162_rn(c[part][2], c[part][3]);
+        *reinterpret_cast<uint2*>(dst + part * DN_QK_SIZE) = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+    }
+    if (lane == 0) {
         const float bb = bf2f(proj[(size_t)t * ldp + DN_CONV_CH + DN_V_SIZE + h]);
         const float aa = bf2f(proj[(size_t)t * ldp + DN_CONV_CH + DN_V_SIZE + DN_HEADS + h]);
         beta[t * DN_HEADS + h] = rbf(sigmoid_f(bb));
@@ -231,9 +242,9 @@ __device__ __forceinline__ void load_at_split(const float* M, int ld, int m0, in
 }
 
 // ---- chunk-local part of the gated delta rule: one CTA (16 warps) per (chunk, head) --------------
-// Per chunk of 64 tokens (zero padded): gc = cumsum(g); T = (I + tril(-(k beta) k^T * decay, -1))^-1 by forward
-// substitution; vprime = T (v beta); kcd = T (k beta exp(gc)); aqk = tril(q k^T * decay).  f32 throughout; the four
-// matrix products (k k^T, q k^T, T v, T k) are 3xTF32 tensor-core tiles, the triangular solve stays on the CUDA cores.
+// Per chunk of 64 tokens (zero padded): gc = cumsum(g); T = (I + tril((k beta) k^T * decay, -1))^-1 (a unit lower triangular
+// solve); vprime = T (v beta); kcd = T (k beta exp(gc)); aqk = tril(q k^T * decay).  f32 throughout; the four matrix products
+// (k k^T, q k^T, T v, T k) are 3xTF32 tensor-core tiles; the triangular solve runs on the CUDA cores in 16 x 16 blocks.
 struct ChunkScratch {          // one record per (head, chunk), floats; every array starts on a 16-byte boundary
     float vprime[DN_CHUNK][DN_V];
     float kcd[DN_CHUNK][DN_K];
@@ -248,7 +259,7 @@ constexpr int CL_THREADS = 512;
 constexpr int CL_LD = DN_K + 4;                          // q, k: A operands (row-major) and, for k, the transposed B operand: bank = 4 g + t
 constexpr int CL_LDB = DN_K + 8;                         // v beta, k beta exp(gc): B operands [token][dim]: bank = 8 t + g
 constexpr int CL_LDA = DN_CHUNK + 4;                     // T: A operand of the last two products
-constexpr int CHUNK_LOCAL_SMEM = (2 * DN_CHUNK * CL_LD + 2 * DN_CHUNK * CL_LDB + DN_CHUNK * CL_LDA + 3 * DN_CHUNK) * 4;
+constexpr int CHUNK_LOCAL_SMEM = (2 * DN_CHUNK * CL_LD + 2 * DN_CHUNK * CL_LDB + 2 * DN_CHUNK * CL_LDA + 3 * 256 + 3 * DN_CHUNK) * 4;
 
 static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(const bf16* __restrict__ qkv, const float* __restrict__ beta,
                                                                        const float* __restrict__ g, ChunkScratch* __restrict__ scratch,
@@ -259,8 +270,10 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
     float* sk = sq + DN_CHUNK * CL_LD;               // [64][CL_LD]   k
     float* sv = sk + DN_CHUNK * CL_LD;               // [64][CL_LDB]  v * beta
     float* skb = sv + DN_CHUNK * CL_LDB;             // [64][CL_LDB]  k * beta * exp(gc)
-    float* sa = skb + DN_CHUNK * CL_LDB;             // [64][CL_LDA]  A, then T
-    float* sb = sa + DN_CHUNK * CL_LDA;
+    float* sa = skb + DN_CHUNK * CL_LDB;             // [64][CL_LDA]  N = -(k beta) k^T * decay, strictly lower
+    float* sx = sa + DN_CHUNK * CL_LDA;              // [64][CL_LDA]  T = (I - N)^-1
+    float* sw = sx + DN_CHUNK * CL_LDA;              // [3][16][16]   block products of the inversion
+    float* sb = sw + 3 * 256;
     float* sg = sb + DN_CHUNK;      // cumulative log-decay
     float* se = sg + DN_CHUNK;      // exp(gc)
     const int c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -351,34 +364,70 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
         }
     }
     __syncthreads();
-    // forward substitution, row by row: row_i[:i] += sum_{j<i} row_i[j] * A[j][:i]  (rows j < i already final).
-    // Only 64 threads take part, so the 126 hand-offs use a 64-thread named barrier; the other warps wait below.
-    if (tid < DN_CHUNK) {
-        for (int i = 1; i < DN_CHUNK; ++i) {
+    // T = (I - N)^-1 with N = sa (strictly lower triangular), in 16 x 16 blocks.
+    //   diagonal blocks: forward substitution inside the block, row by row (row_i[:i] += sum_{j<i} row_i[j] * row_j[:i], rows
+    //   j < i final), one warp per block, so its 15 steps need no CTA barrier;
+    //   blocks below: T_ij = T_ii * sum_{k = j}^{i-1} N_ik T_kj, one block diagonal at a time (three levels), each level two small
+    //   products on the CUDA cores.  The same triangular solve as the row-by-row loop of the chunk-64 formulation, summed in
+    //   block order.
+    if (warp < 4) {
+        float* blk = sa + (warp * 16) * CL_LDA + warp * 16;
+        const int j = lane & 15;
+        for (int i = 1; i < 16; ++i) {
             float nv = 0.f;
-            if (tid < i) {
-                // four independent partial sums keep four pairs of shared-memory loads in flight
-                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-                const float* ri = sa + i * CL_LDA;
-                const float* cj = sa + tid;
-                int j = 0;
-                for (; j + 4 <= i; j += 4) {
-                    a0 = fmaf(ri[j], cj[j * CL_LDA], a0);
-                    a1 = fmaf(ri[j + 1], cj[(j + 1) * CL_LDA], a1);
-                    a2 = fmaf(ri[j + 2], cj[(j + 2) * CL_LDA], a2);
-                    a3 = fmaf(ri[j + 3], cj[(j + 3) * CL_LDA], a3);
+            if (lane < i) {
+                float a0 = 0.f, a1 = 0.f;
+                const float* ri = blk + i * CL_LDA;
+                int k = 0;
+                for (; k + 2 <= i; k += 2) {
+                    a0 = fmaf(ri[k], blk[k * CL_LDA + j], a0);
+                    a1 = fmaf(ri[k + 1], blk[(k + 1) * CL_LDA + j], a1);
                 }
-                for (; j < i; ++j) a0 = fmaf(ri[j], cj[j * CL_LDA], a0);
-                nv = ri[tid] + ((a0 + a1) + (a2 + a3));
+                if (k < i) a0 = fmaf(ri[k], blk[k * CL_LDA + j], a0);
+                nv = ri[j] + (a0 + a1);
             }
-            asm volatile("bar.sync 1, 64;" ::: "memory");
-            if (tid < i) sa[i * CL_LDA + tid] = nv;
-            asm volatile("bar.sync 1, 64;" ::: "memory");
+            __syncwarp();
+            if (lane < i) blk[i * CL_LDA + j] = nv;
+            __syncwarp();
+        }
+        // the finished block, with its unit diagonal and zero upper triangle, into T
+        for (int e = lane; e < 256; e += 32) {
+            const int i = e >> 4, jj = e & 15;
+            sx[(warp * 16 + i) * CL_LDA + warp * 16 + jj] = (jj < i) ? blk[i * CL_LDA + jj] : (jj == i ? 1.0f : 0.f);
         }
     }
     __syncthreads();
-    if (tid < DN_CHUNK) sa[tid * CL_LDA + tid] = 1.0f;
-    __syncthreads();
+    for (int d = 1; d < 4; ++d) {
+        const int nblk = 4 - d;
+        // W_b = sum_{k = j}^{i-1} N_ik T_kj for the blocks (i, j) = (b + d, b)
+        for (int e = tid; e < nblk * 256; e += CL_THREADS) {
+            const int b = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+            const float* nrow = sa + ((b + d) * 16 + r) * CL_LDA + b * 16;       // N[i-row][columns of blocks j .. i-1]
+            const float* tcol = sx + (b * 16) * CL_LDA + b * 16 + cc;             // T[rows of blocks j .. i-1][column]
+            float a0 = 0.f, a1 = 0.f;
+#pragma unroll 4
+            for (int k = 0; k < 16 * d; k += 2) {
+                a0 = fmaf(nrow[k], tcol[k * CL_LDA], a0);
+                a1 = fmaf(nrow[k + 1], tcol[(k + 1) * CL_LDA], a1);
+            }
+            sw[e] = a0 + a1;
+        }
+        __syncthreads();
+        // T_ij = T_ii W_b (T_ii lower triangular with unit diagonal)
+        for (int e = tid; e < nblk * 256; e += CL_THREADS) {
+            const int b = e >> 8, r = (e >> 4) & 15, cc = e & 15;
+            const float* trow = sx + ((b + d) * 16 + r) * CL_LDA + (b + d) * 16;
+            const float* wc = sw + b * 256 + cc;
+            float a0 = 0.f, a1 = 0.f;
+            for (int k = 0; k + 2 <= r; k += 2) {
+                a0 = fmaf(trow[k], wc[k * 16], a0);
+                a1 = fmaf(trow[k + 1], wc[(k + 1) * 16], a1);
+            }
+            if (r & 1) a0 = fmaf(trow[r - 1], wc[(r - 1) * 16], a0);
+            sx[((b + d) * 16 + r) * CL_LDA + b * 16 + cc] = wc[r * 16] + (a0 + a1);
+        }
+        __syncthreads();
+    }
     // ---- vprime = T (v beta) (warps 0-7), kcd = T (k beta exp(gc)) (warps 8-15): 64 x 128 x 64 with T lower triangular.  A warp
     // takes a quarter of the 128 columns and two row tiles whose k ranges add up to the same length: (0, 3) or (1, 2).
     {
@@ -395,7 +444,7 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
                 for (int r = 0; r < 4; ++r) acc[n][r] = 0.f;
             for (int k0 = 0; k0 < 16 * (mt + 1); k0 += 8) {
                 uint32_t ah[4], al[4];
-                load_a_split(sa, CL_LDA, mt * 16, k0, ah, al);
+                load_a_split(sx, CL_LDA, mt * 16, k0, ah, al);
 #pragma unroll
                 for (int n = 0; n < 4; ++n) {
                     const float* br = Bm + (k0 + t4) * CL_LDB + nq * 32 + n * 8 + gq;       // B(k, n) = Bm[token k][dim n]
@@ -801,6 +850,188 @@ static __global__ void __launch_bounds__(256, 1) pf_attention_mma_kernel(const b
 #pragma unroll
         for (int nt = 0; nt < FA_HEAD_DIM / 8; ++nt) {
             const int d = nt * 8 + 2 * c;
+            const uint32_t gr = *reinterpret_cast<const uint32_t*>(gate + d);
+            const __nv_bfloat162 pr = __halves2bfloat162(f2bf(rbf(o[nt][2 * hf]) * rbf(sigmoid_f(bf_lo(gr)))), f2bf(rbf(o[nt][2 * hf + 1]) * rbf(sigmoid_f(bf_hi(gr)))));
+            *reinterpret_cast<__nv_bfloat162*>(dst + d) = pr;
+        }
+    }
+}
+
+// ---- the same attention for short prompts: keys of a chunk split over four warps -------------------------------
+// With few query blocks the kernel above leaves most SMs idle and each warp walks the whole key range alone.  Here a CTA takes
+// 8 queries x 4 heads = 32 rows (two 16-row tiles) and 8 warps = (row tile rt, key quarter ks): per 64-key chunk a warp
+// computes the scores of its 16 keys only (its Q fragments stay in registers), so the chain per chunk is a quarter as long
+// and S / 8 x 2 CTAs fill the machine at S ~ 500.  Pass 1 gives each warp the maximum and normaliser of its keys; the four
+// partial pairs of a row tile are merged through shared memory.  In pass 2 each warp rounds its P = bf16(exp(s - m) / l)
+// values (the same rounding points as above) into a shared [16 x 64] tile, and after a barrier of the row tile's four
+// warps each accumulates P.V for its own quarter of the head dimension, so no partial outputs have to be summed.
+// K (and V in pass 2) chunks arrive by cp.async into two buffers, one __syncthreads per chunk.
+constexpr int ATS_Q = 8, ATS_ROWS = ATS_Q * FA_GQA, ATS_KEYS = 64, ATS_LD = FA_HEAD_DIM + 8, ATS_PLD = ATS_KEYS + 8;
+constexpr int ATS_SMEM = (ATS_ROWS * ATS_LD + 4 * ATS_KEYS * ATS_LD + 2 * 16 * ATS_PLD) * 2 + 2 * 4 * 16 * 2 * 4;
+constexpr int ATS_MAX_S = 1024;          // longer prompts have enough query blocks for the kernel above, which re-reads K / V less
+
+__device__ __forceinline__ void ats_cp16(bf16* dst, const bf16* src, bool valid) {
+    const int n = valid ? 16 : 0;        // 0 source bytes: the 16 destination bytes are zero-filled
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src), "r"(n) : "memory");
+}
+
+static __global__ void __launch_bounds__(256, 1) pf_attention_split_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k_cache,
+                                                                    const bf16* __restrict__ v_cache, const bf16* __restrict__ proj, int ldp,
+                                                                    bf16* __restrict__ out, int S, int max_seq) {
+    pdl_wait();
+    extern __shared__ __align__(16) unsigned char ats_sm[];
+    bf16* Qs = reinterpret_cast<bf16*>(ats_sm);
+    bf16* KV = Qs + ATS_ROWS * ATS_LD;                    // [buffer 2][K, V][64][LD]
+    bf16* Ps = KV + 4 * ATS_KEYS * ATS_LD;                // [row tile 2][16][PLD]
+    float* ML = reinterpret_cast<float*>(Ps + 2 * 16 * ATS_PLD);   // [row tile 2][ks 4][16 rows][m, l]
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+    const int rt = warp >> 2, ks = warp & 3;
+    const int blk = (int)gridDim.x - 1 - (int)blockIdx.x;          // long blocks first
+    const int kvh = blockIdx.y, q0 = blk * ATS_Q;
+    const bf16* kb = k_cache + (size_t)kvh * max_seq * FA_HEAD_DIM;
+    const bf16* vb = v_cache + (size_t)kvh * max_seq * FA_HEAD_DIM;
+    const int t_last = min(q0 + ATS_Q, S) - 1;
+    const int nchunks = t_last / ATS_KEYS + 1, nitems = 2 * nchunks;
+
+    auto stage = [&](int item) {
+        const int pass = item >= nchunks, j0 = (pass ? item - nchunks : item) * ATS_KEYS;
+        bf16* kd = KV + (size_t)(item & 1) * 2 * ATS_KEYS * ATS_LD;
+        bf16* vd = kd + ATS_KEYS * ATS_LD;
+        for (int i = tid; i < ATS_KEYS * (FA_HEAD_DIM / 8); i += 256) {
+            const int kk = i / (FA_HEAD_DIM / 8), c8 = i % (FA_HEAD_DIM / 8);
+            const bool ok = j0 + kk < S;
+            const size_t off = (size_t)(ok ? j0 + kk : 0) * FA_HEAD_DIM + c8 * 8;
+            ats_cp16(kd + kk * ATS_LD + c8 * 8, kb + off, ok);
+            if (pass) ats_cp16(vd + kk * ATS_LD + c8 * 8, vb + off, ok);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+
+    stage(0);
+    for (int i = tid; i < ATS_ROWS * (FA_HEAD_DIM / 8); i += 256) {
+        const int r = i / (FA_HEAD_DIM / 8), c8 = i % (FA_HEAD_DIM / 8), t = q0 + r / FA_GQA;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (t < S) v = *reinterpret_cast<const uint4*>(q + (size_t)t * FA_Q_SIZE + (kvh * FA_GQA + r % FA_GQA) * FA_HEAD_DIM + c8 * 8);
+        *reinterpret_cast<uint4*>(Qs + r * ATS_LD + c8 * 8) = v;
+    }
+    __syncthreads();
+    uint32_t qf[FA_HEAD_DIM / 16][4];
+#pragma unroll
+    for (int kk = 0; kk < FA_HEAD_DIM / 16; ++kk) ldsm_x4(qf[kk], Qs + (rt * 16 + (lane & 15)) * ATS_LD + kk * 16 + (lane >> 4) * 8);
+
+    const int r0 = rt * 16 + g, r1 = r0 + 8;                       // this thread's two rows
+    const int t0 = q0 + r0 / FA_GQA, t1 = q0 + r1 / FA_GQA;
+    const int t_max_rt = min(q0 + (rt * 16 + 15) / FA_GQA, S - 1);  // last query of this row tile
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float o[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) { o[nt][0] = 0.f; o[nt][1] = 0.f; o[nt][2] = 0.f; o[nt][3] = 0.f; }
+    bf16* Pt = Ps + rt * 16 * ATS_PLD;
+
+    for (int item = 0; item < nitems; ++item) {
+        const int pass = item >= nchunks, j0 = (pass ? item - nchunks : item) * ATS_KEYS;
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        if (item == nchunks) {                                    // end of pass 1: publish this warp's (m, l) before the barrier
+            if (c == 0) {
+                float* d = ML + ((rt * 4 + ks) * 16) * 2;
+                d[2 * g] = m0; d[2 * g + 1] = l0; d[2 * (g + 8)] = m1; d[2 * (g + 8) + 1] = l1;
+            }
+        }
+        __syncthreads();                                          // this item's chunk is in; every warp is done with the previous one
+        if (item + 1 < nitems) stage(item + 1);
+        if (item == nchunks) {                                    // merge the four key quarters' partial softmax statistics
+            float M0 = -INFINITY, M1 = -INFINITY;
+#pragma unroll
+            for (int k2 = 0; k2 < 4; ++k2) {
+                const float* d = ML + ((rt * 4 + k2) * 16) * 2;
+                M0 = fmaxf(M0, d[2 * g]); M1 = fmaxf(M1, d[2 * (g + 8)]);
+            }
+            float L0 = 0.f, L1 = 0.f;
+#pragma unroll
+            for (int k2 = 0; k2 < 4; ++k2) {
+                const float* d = ML + ((rt * 4 + k2) * 16) * 2;
+                if (d[2 * g] != -INFINITY) L0 += d[2 * g + 1] * expf(d[2 * g] - M0);
+                if (d[2 * (g + 8)] != -INFINITY) L1 += d[2 * (g + 8) + 1] * expf(d[2 * (g + 8)] - M1);
+            }
+            m0 = M0; m1 = M1; l0 = L0; l1 = L1;
+        }
+        if (j0 > t_max_rt) continue;                              // chunk beyond this row tile's causal range (uniform per row tile)
+        const bf16* Kc = KV + (size_t)(item & 1) * 2 * ATS_KEYS * ATS_LD;
+        const bf16* Vc = Kc + ATS_KEYS * ATS_LD;
+        // scores of the 16 rows against this warp's 16 keys
+        float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        const bool live = j0 + ks * 16 <= t_max_rt;               // any unmasked key in this quarter
+        if (live) {
+#pragma unroll
+            for (int kk = 0; kk < FA_HEAD_DIM / 16; ++kk) {
+                uint32_t b[4];
+                ldsm_x4(b, Kc + (ks * 16 + (lane & 7) + 8 * (lane >> 4)) * ATS_LD + kk * 16 + 8 * ((lane >> 3) & 1));
+                mma_16816(sacc[0], qf[kk], b[0], b[1]);
+                mma_16816(sacc[1], qf[kk], b[2], b[3]);
+            }
+        }
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int j = j0 + ks * 16 + nt * 8 + 2 * c + (e & 1);
+                const int tr = (e < 2) ? t0 : t1;
+                sacc[nt][e] = (live && j <= tr && tr < S) ? rbf(sacc[nt][e]) * 0.0625f : -INFINITY;
+            }
+        if (!pass) {
+            float cm0 = fmaxf(fmaxf(sacc[0][0], sacc[0][1]), fmaxf(sacc[1][0], sacc[1][1]));
+            float cm1 = fmaxf(fmaxf(sacc[0][2], sacc[0][3]), fmaxf(sacc[1][2], sacc[1][3]));
+            cm0 = fmaxf(cm0, __shfl_xor_sync(0xffffffffu, cm0, 1)); cm0 = fmaxf(cm0, __shfl_xor_sync(0xffffffffu, cm0, 2));
+            cm1 = fmaxf(cm1, __shfl_xor_sync(0xffffffffu, cm1, 1)); cm1 = fmaxf(cm1, __shfl_xor_sync(0xffffffffu, cm1, 2));
+            const float n0 = fmaxf(m0, cm0), n1 = fmaxf(m1, cm1);
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                if (n0 != -INFINITY) s0 += expf(sacc[nt][0] - n0) + expf(sacc[nt][1] - n0);
+                if (n1 != -INFINITY) s1 += expf(sacc[nt][2] - n1) + expf(sacc[nt][3] - n1);
+            }
+            s0 += __shfl_xor_sync(0xffffffffu, s0, 1); s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
+            s1 += __shfl_xor_sync(0xffffffffu, s1, 1); s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
+            l0 = (m0 == -INFINITY ? 0.f : l0 * expf(m0 - n0)) + s0;
+            l1 = (m1 == -INFINITY ? 0.f : l1 * expf(m1 - n1)) + s1;
+            m0 = n0; m1 = n1;
+        } else {
+            // P of this warp's 16 keys into the row tile's shared [16 x 64] tile
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+                const float* sv = sacc[nt];
+                const float p00 = (sv[0] == -INFINITY) ? 0.f : expf(sv[0] - m0) / l0, p01 = (sv[1] == -INFINITY) ? 0.f : expf(sv[1] - m0) / l0;
+                const float p10 = (sv[2] == -INFINITY) ? 0.f : expf(sv[2] - m1) / l1, p11 = (sv[3] == -INFINITY) ? 0.f : expf(sv[3] - m1) / l1;
+                *reinterpret_cast<__nv_bfloat162*>(Pt + g * ATS_PLD + ks * 16 + nt * 8 + 2 * c) = __floats2bfloat162_rn(p00, p01);
+                *reinterpret_cast<__nv_bfloat162*>(Pt + (g + 8) * ATS_PLD + ks * 16 + nt * 8 + 2 * c) = __floats2bfloat162_rn(p10, p11);
+            }
+            asm volatile("bar.sync %0, 128;" ::"r"(1 + rt) : "memory");      // the four warps of this row tile
+            // P.V for head dimensions [64 ks, 64 ks + 64)
+            const int nk = min(4, (t_max_rt - j0) / 16 + 1);      // 16-key steps with any unmasked key
+            for (int k2 = 0; k2 < nk; ++k2) {
+                uint32_t a[4];
+                ldsm_x4(a, Pt + (lane & 15) * ATS_PLD + k2 * 16 + (lane >> 4) * 8);
+#pragma unroll
+                for (int np = 0; np < 4; ++np) {
+                    uint32_t b[4];
+                    ldsm_x4_trans(b, Vc + (k2 * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * ATS_LD + ks * 64 + np * 16 + 8 * (lane >> 4));
+                    mma_16816(o[2 * np], a, b[0], b[1]);
+                    mma_16816(o[2 * np + 1], a, b[2], b[3]);
+                }
+            }
+        }
+    }
+    // output: bf16(P.V) * bf16(sigmoid(gate)), rows r0 (o[.][0..1]) and r1 (o[.][2..3]), this warp's 64 head dimensions
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+        const int r = hf ? r1 : r0, t = hf ? t1 : t0;
+        if (t >= S) continue;
+        const int head = kvh * FA_GQA + r % FA_GQA;
+        const bf16* gate = proj + (size_t)t * ldp + head * 2 * FA_HEAD_DIM + FA_HEAD_DIM;
+        bf16* dst = out + (size_t)t * FA_Q_SIZE + head * FA_HEAD_DIM;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+            const int d = ks * 64 + nt * 8 + 2 * c;
             const uint32_t gr = *reinterpret_cast<const uint32_t*>(gate + d);
             const __nv_bfloat162 pr = __halves2bfloat162(f2bf(rbf(o[nt][2 * hf]) * rbf(sigmoid_f(bf_lo(gr)))), f2bf(rbf(o[nt][2 * hf + 1]) * rbf(sigmoid_f(bf_hi(gr)))));
             *reinterpret_cast<__nv_bfloat162*>(dst + d) = pr;
