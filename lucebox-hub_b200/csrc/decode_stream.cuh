@@ -15,7 +15,6 @@
 
 namespace q35 {
 
-typedef unsigned long long u64;
 
 constexpr int MAX_CTX = 32768;          // longest context the decode scratch is sized for
 constexpr int ATT_MAX_CHUNKS = 64;      // split-KV factor of decode attention (chunks per kv head)
@@ -80,43 +79,6 @@ struct DecodeArgs {
     int tma_period;           // minimum SM clocks between two weight-tile copies of one CTA (paces the HBM stream)
     unsigned epoch_base;      // epochs used by this launch: epoch_base + 32*step + {1..24 layer, 25 LM}
 };
-
-// ---- mbarrier / TMA bulk primitives (inline PTX) ----------------------------------------------
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_fence_init() {
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ u64 l2_policy_evict_first() {
-    u64 p;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-    return p;
-}
-// 1-D bulk copy global -> this CTA's shared memory, completion counted on `bar`.
-// Both addresses and the size are multiples of 16 bytes.  No multicast.
-__device__ __forceinline__ void tma_load_1d(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar, u64 policy) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
-        ::"r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(policy) : "memory");
-}
 
 // ---- flagged words --------------------------------------------------------------------------------
 __device__ __forceinline__ u64 ld_word(const u64* p) {

@@ -76,6 +76,8 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
         attr_done.mark();
     }
     const int nchunks = (S + DN_CHUNK - 1) / DN_CHUNK;
+    int* err_word = (int*)get_workspace();            // the device status word the bounded waits report to
+    if (!err_word) return QWEN35_ERR_CUDA;
     // library scratch: the chunk-local results, then the NVFP4 operand of the activations (packed rows padded to 128 + scale
     // atoms) and one row of bf16 logits for the tensor-core FP4 head
     const size_t chunk_bytes = ((size_t)DN_HEADS * nchunks * sizeof(ChunkScratch) + 255) & ~(size_t)255;
@@ -126,7 +128,7 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
             Q35_CUDA_OK(pdl_launch(pf_conv_state_kernel, (DN_CONV_CH + 255) / 256, 256, 0, stream, a.proj_buf, ldp, a.conv_bufs + (size_t)i_dn * DN_CONV_CH * 4, S));
             Q35_CUDA_OK(pdl_launch(pf_dn_chunk_local_kernel, dim3(nchunks, DN_HEADS), CL_THREADS, CHUNK_LOCAL_SMEM, stream, a.proj_buf2, a.beta_buf, a.alpha_buf, scratch, S, nchunks));
             Q35_CUDA_OK(pdl_launch(pf_dn_chunk_scan_kernel, dim3(DN_HEADS, DN_V / SCAN_VW), SCAN_THREADS, CHUNK_SCAN_SMEM, stream, 
-                scratch, a.dn_out_buf, a.dn_states + (size_t)i_dn * DN_HEADS * DN_V * DN_K, S, nchunks));
+                scratch, a.dn_out_buf, a.dn_states + (size_t)i_dn * DN_HEADS * DN_V * DN_K, S, nchunks, err_word));
             Q35_CUDA_OK(pdl_launch(pf_gated_norm_kernel, (S * DN_HEADS + 7) / 8, 256, 0, stream, a.dn_out_buf, a.proj_buf, ldp, (const bf16*)L.p[DN_NORM], a.attn_buf, S));
             g_launches.fetch_add(5);
             w_out = (const bf16*)L.p[DN_OUT]; w_post = (const bf16*)L.p[DN_POST_NORM]; w_down = (const bf16*)L.p[DN_DOWN];

@@ -204,11 +204,10 @@ static __global__ void pf_conv_state_kernel(const bf16* __restrict__ proj, int l
 // a_lo b_hi + a_hi b_lo + a_hi b_hi with f32 accumulation ("3xTF32"): about 21 bits per operand, f32 sums.
 // Fragment layout of mma.m16n8k8 (g = lane / 4, t = lane % 4):  A (16x8, row):  a0 (g, t)  a1 (g+8, t)  a2 (g, t+4)  a3 (g+8, t+4);
 // B (8x8, k x n):  b0 (t, g)  b1 (t+4, g);   C (16x8):  c0 (g, 2t)  c1 (g, 2t+1)  c2 (g+8, 2t)  c3 (g+8, 2t+1).
-__device__ __forceinline__ uint32_t tf32_of(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return r;
-}
+// f32 -> tf32, round to nearest with ties away from zero: what cvt.rna.tf32.f32 returns for finite values, written as an
+// add and a mask on the bit pattern (sign-magnitude, so adding half a last place to the magnitude rounds it).  The
+// conversion instruction runs at a fraction of the integer rate and bounded these kernels.
+__device__ __forceinline__ uint32_t tf32_of(float x) { return (__float_as_uint(x) + 0x1000u) & 0xffffe000u; }
 __device__ __forceinline__ void tf32_split(float x, uint32_t& hi, uint32_t& lo) {
     hi = tf32_of(x);
     lo = tf32_of(x - __uint_as_float(hi));
@@ -218,12 +217,15 @@ __device__ __forceinline__ void mma_tf32(float (&c)[4], const uint32_t (&a)[4], 
                  : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
                  : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
-__device__ __forceinline__ void mma_3xtf32(float (&c)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4], uint32_t bh0, uint32_t bh1,
-                                           uint32_t bl0, uint32_t bl1) {
-    mma_tf32(c, al, bh0, bh1);
-    mma_tf32(c, ah, bl0, bl1);
-    mma_tf32(c, ah, bh0, bh1);
+// One accumulator per term: three independent dependency chains instead of one three times as long (the kernels below are
+// bound by the latency of back-to-back mma on one accumulator, not by issue slots); the terms are summed small to large.
+__device__ __forceinline__ void mma_3xtf32_terms(float (&c)[3][4], const uint32_t (&ah)[4], const uint32_t (&al)[4], uint32_t bh0, uint32_t bh1,
+                                                 uint32_t bl0, uint32_t bl1) {
+    mma_tf32(c[0], al, bh0, bh1);
+    mma_tf32(c[1], ah, bl0, bl1);
+    mma_tf32(c[2], ah, bh0, bh1);
 }
+__device__ __forceinline__ float sum_terms(const float (&c)[3][4], int r) { return (c[0][r] + c[1][r]) + c[2][r]; }
 // A fragment of a row-major f32 matrix in shared memory (rows m0.., columns k0..), split into hi / lo
 __device__ __forceinline__ void load_a_split(const float* A, int ld, int m0, int k0, uint32_t (&ah)[4], uint32_t (&al)[4]) {
     const int g = (threadIdx.x & 31) >> 2, t = threadIdx.x & 3;
@@ -245,15 +247,23 @@ __device__ __forceinline__ void load_at_split(const float* M, int ld, int m0, in
 // Per chunk of 64 tokens (zero padded): gc = cumsum(g); T = (I + tril((k beta) k^T * decay, -1))^-1 (a unit lower triangular
 // solve); vprime = T (v beta); kcd = T (k beta exp(gc)); aqk = tril(q k^T * decay).  f32 throughout; the four matrix products
 // (k k^T, q k^T, T v, T k) are 3xTF32 tensor-core tiles; the triangular solve runs on the CUDA cores in 16 x 16 blocks.
+// The record the scan kernel reads.  Its arrays have the row pitches of the scan's shared-memory operands (padded against
+// bank conflicts) and vprime is stored by 16-column slice, so that each operand of a scan CTA is ONE contiguous block
+// and moves with a single bulk copy; the pad columns are never read by an mma.
+constexpr int SCAN_VW = 16;                 // value columns per scan CTA
+constexpr int SCAN_LDA = DN_K + 4;          // kcd, qs: row-major A operands, bank = 4 g + t
+constexpr int SCAN_LDT = DN_K + 8;          // ks: read as its transpose, bank = 8 t + g
+constexpr int SCAN_LDQ = DN_CHUNK + 4;      // aqk
 struct ChunkScratch {          // one record per (head, chunk), floats; every array starts on a 16-byte boundary
-    float vprime[DN_CHUNK][DN_V];
-    float kcd[DN_CHUNK][DN_K];
-    float qs[DN_CHUNK][DN_K];      // q / sqrt(128) * exp(gc_i): the scan's left operand of q S
-    float ks[DN_CHUNK][DN_K];      // k * exp(gc_last - gc_i):   the scan's left operand of the state update
-    float aqk[DN_CHUNK][DN_CHUNK];
+    float vprime[DN_V / SCAN_VW][DN_CHUNK][SCAN_VW];
+    float kcd[DN_CHUNK][SCAN_LDA];
+    float qs[DN_CHUNK][SCAN_LDA];      // q / sqrt(128) * exp(gc_i): the scan's left operand of q S
+    float ks[DN_CHUNK][SCAN_LDT];      // k * exp(gc_last - gc_i):   the scan's left operand of the state update
+    float aqk[DN_CHUNK][SCAN_LDQ];
     float gc[DN_CHUNK];
     float eg_last[4];              // [0] = exp(gc_last)
 };
+static_assert(sizeof(ChunkScratch) % 16 == 0, "records must keep 16-byte alignment");
 
 constexpr int CL_THREADS = 512;
 constexpr int CL_LD = DN_K + 4;                          // q, k: A operands (row-major) and, for k, the transposed B operand: bank = 4 g + t
@@ -286,16 +296,22 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
         sb[tid] = (t < S) ? beta[t * DN_HEADS + h] : 0.f;
         sg[tid] = (t < S) ? g[t * DN_HEADS + h] : 0.f;
     }
-    for (int e = tid; e < DN_CHUNK * DN_K; e += CL_THREADS) {
-        const int i = e >> 7, d = e & 127, t = t0 + i;
-        float qv = 0.f, kv = 0.f, vv = 0.f;
+    for (int e = tid; e < DN_CHUNK * (DN_K / 8); e += CL_THREADS) {          // eight dimensions (16 bytes of bf16) per step
+        const int i = e >> 4, d = (e & 15) * 8, t = t0 + i;
+        uint4 qr = make_uint4(0, 0, 0, 0), kr = qr, vr = qr;
         if (t < S) {
             const bf16* row = qkv + (size_t)t * DN_CONV_CH + h * DN_K + d;
-            qv = bf2f(row[0]) * 0.08838834764831845f;
-            kv = bf2f(row[DN_QK_SIZE]);
-            vv = bf2f(row[2 * DN_QK_SIZE]);
+            qr = *reinterpret_cast<const uint4*>(row);
+            kr = *reinterpret_cast<const uint4*>(row + DN_QK_SIZE);
+            vr = *reinterpret_cast<const uint4*>(row + 2 * DN_QK_SIZE);
         }
-        sq[i * CL_LD + d] = qv; sk[i * CL_LD + d] = kv; sv[i * CL_LDB + d] = vv;
+        const float qs_ = 0.08838834764831845f;
+        *reinterpret_cast<float4*>(sq + i * CL_LD + d) = make_float4(bf_lo(qr.x) * qs_, bf_hi(qr.x) * qs_, bf_lo(qr.y) * qs_, bf_hi(qr.y) * qs_);
+        *reinterpret_cast<float4*>(sq + i * CL_LD + d + 4) = make_float4(bf_lo(qr.z) * qs_, bf_hi(qr.z) * qs_, bf_lo(qr.w) * qs_, bf_hi(qr.w) * qs_);
+        *reinterpret_cast<float4*>(sk + i * CL_LD + d) = make_float4(bf_lo(kr.x), bf_hi(kr.x), bf_lo(kr.y), bf_hi(kr.y));
+        *reinterpret_cast<float4*>(sk + i * CL_LD + d + 4) = make_float4(bf_lo(kr.z), bf_hi(kr.z), bf_lo(kr.w), bf_hi(kr.w));
+        *reinterpret_cast<float4*>(sv + i * CL_LDB + d) = make_float4(bf_lo(vr.x), bf_hi(vr.x), bf_lo(vr.y), bf_hi(vr.y));
+        *reinterpret_cast<float4*>(sv + i * CL_LDB + d + 4) = make_float4(bf_lo(vr.z), bf_hi(vr.z), bf_lo(vr.w), bf_hi(vr.w));
     }
     __syncthreads();
     if (tid == 0) {                 // sequential cumsum, as torch.cumsum does
@@ -307,13 +323,16 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
     __syncthreads();
     {   // operands of the scan that depend on this chunk only; v * beta and k * beta * exp(gc) for the products below
         const float g_last = sg[DN_CHUNK - 1];
-        for (int e = tid; e < DN_CHUNK * DN_K; e += CL_THREADS) {
-            const int i = e >> 7, d = e & 127;
-            const float kv = sk[i * CL_LD + d];
-            out.qs[i][d] = sq[i * CL_LD + d] * se[i];
-            out.ks[i][d] = kv * expf(g_last - sg[i]);
-            sv[i * CL_LDB + d] *= sb[i];
-            skb[i * CL_LDB + d] = (kv * sb[i]) * se[i];
+        for (int e = tid; e < DN_CHUNK * (DN_K / 4); e += CL_THREADS) {
+            const int i = e >> 5, d = (e & 31) * 4;
+            const float4 kv = *reinterpret_cast<const float4*>(sk + i * CL_LD + d), qv = *reinterpret_cast<const float4*>(sq + i * CL_LD + d);
+            float4 vv = *reinterpret_cast<const float4*>(sv + i * CL_LDB + d);
+            const float ei = se[i], kd = expf(g_last - sg[i]), bi = sb[i];
+            *reinterpret_cast<float4*>(&out.qs[i][d]) = make_float4(qv.x * ei, qv.y * ei, qv.z * ei, qv.w * ei);
+            *reinterpret_cast<float4*>(&out.ks[i][d]) = make_float4(kv.x * kd, kv.y * kd, kv.z * kd, kv.w * kd);
+            vv.x *= bi; vv.y *= bi; vv.z *= bi; vv.w *= bi;
+            *reinterpret_cast<float4*>(sv + i * CL_LDB + d) = vv;
+            *reinterpret_cast<float4*>(skb + i * CL_LDB + d) = make_float4((kv.x * bi) * ei, (kv.y * bi) * ei, (kv.z * bi) * ei, (kv.w * bi) * ei);
         }
         if (tid == 0) out.eg_last[0] = expf(g_last);
     }
@@ -326,11 +345,11 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
         const int ntn = (u == 2 || u >= 5) ? 2 : 3;
         const bool is_q = warp >= 8;
         const float* A = is_q ? sq : sk;
-        float acc[3][4];
+        float acc3[3][3][4];
 #pragma unroll
         for (int n = 0; n < 3; ++n)
 #pragma unroll
-            for (int r = 0; r < 4; ++r) acc[n][r] = 0.f;
+            for (int r = 0; r < 12; ++r) acc3[n][r >> 2][r & 3] = 0.f;
 #pragma unroll 2
         for (int k0 = 0; k0 < DN_K; k0 += 8) {
             uint32_t ah[4], al[4];
@@ -342,9 +361,14 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
                     uint32_t bh0, bl0, bh1, bl1;
                     tf32_split(br[0], bh0, bl0);
                     tf32_split(br[4], bh1, bl1);
-                    mma_3xtf32(acc[n], ah, al, bh0, bh1, bl0, bl1);
+                    mma_3xtf32_terms(acc3[n], ah, al, bh0, bh1, bl0, bl1);
                 }
         }
+        float acc[3][4];
+#pragma unroll
+        for (int n = 0; n < 3; ++n)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) acc[n][r] = sum_terms(acc3[n], r);
         // A[i][j] = -(beta_i k_i . k_j) * exp(gc_i - gc_j) for j < i, else 0;   aqk[i][j] = (q_i . k_j) * exp(gc_i - gc_j) for j <= i
 #pragma unroll
         for (int n = 0; n < 3; ++n)
@@ -365,36 +389,40 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
     }
     __syncthreads();
     // T = (I - N)^-1 with N = sa (strictly lower triangular), in 16 x 16 blocks.
-    //   diagonal blocks: forward substitution inside the block, row by row (row_i[:i] += sum_{j<i} row_i[j] * row_j[:i], rows
-    //   j < i final), one warp per block, so its 15 steps need no CTA barrier;
+    //   diagonal blocks: forward substitution inside the block (T_ij = N_ij + sum_{j < k < i} N_ik T_kj), one warp per block,
+    //   one lane per column, so its 15 steps need no barrier at all;
     //   blocks below: T_ij = T_ii * sum_{k = j}^{i-1} N_ik T_kj, one block diagonal at a time (three levels), each level two small
     //   products on the CUDA cores.  The same triangular solve as the row-by-row loop of the chunk-64 formulation, summed in
     //   block order.
-    if (warp < 4) {
-        float* blk = sa + (warp * 16) * CL_LDA + warp * 16;
-        const int j = lane & 15;
+    if (warp < 4 && lane < 16) {
+        // lane j solves column j of the block on its own: x_i = N_ij + sum_{j < k < i} N_ik x_k, the x_k in registers, the rows
+        // of N read as broadcasts; no step waits for another lane
+        const float* blk = sa + (warp * 16) * CL_LDA + warp * 16;
+        float x[16];
+        x[0] = 0.f;
+#pragma unroll
         for (int i = 1; i < 16; ++i) {
-            float nv = 0.f;
-            if (lane < i) {
-                float a0 = 0.f, a1 = 0.f;
-                const float* ri = blk + i * CL_LDA;
-                int k = 0;
-                for (; k + 2 <= i; k += 2) {
-                    a0 = fmaf(ri[k], blk[k * CL_LDA + j], a0);
-                    a1 = fmaf(ri[k + 1], blk[(k + 1) * CL_LDA + j], a1);
-                }
-                if (k < i) a0 = fmaf(ri[k], blk[k * CL_LDA + j], a0);
-                nv = ri[j] + (a0 + a1);
+            float nrow[16];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float4 v = *reinterpret_cast<const float4*>(blk + i * CL_LDA + 4 * q);
+                nrow[4 * q] = v.x; nrow[4 * q + 1] = v.y; nrow[4 * q + 2] = v.z; nrow[4 * q + 3] = v.w;
             }
-            __syncwarp();
-            if (lane < i) blk[i * CL_LDA + j] = nv;
-            __syncwarp();
+            float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+            for (int k = 1; k < i; ++k) {
+                if (k & 1) a0 = fmaf(nrow[k], x[k], a0);
+                else a1 = fmaf(nrow[k], x[k], a1);
+            }
+            float nij = 0.f;
+#pragma unroll
+            for (int k = 0; k < 16; ++k) nij = (k == lane) ? nrow[k] : nij;
+            x[i] = (lane < i) ? nij + (a0 + a1) : 0.f;
         }
         // the finished block, with its unit diagonal and zero upper triangle, into T
-        for (int e = lane; e < 256; e += 32) {
-            const int i = e >> 4, jj = e & 15;
-            sx[(warp * 16 + i) * CL_LDA + warp * 16 + jj] = (jj < i) ? blk[i * CL_LDA + jj] : (jj == i ? 1.0f : 0.f);
-        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+            sx[(warp * 16 + i) * CL_LDA + warp * 16 + lane] = (lane < i) ? x[i] : (lane == i ? 1.0f : 0.f);
     }
     __syncthreads();
     for (int d = 1; d < 4; ++d) {
@@ -433,15 +461,15 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
     {
         const int u = warp & 7, nq = u & 3;
         const float* Bm = (warp < 8) ? sv : skb;
-        float (*dst)[DN_K] = (warp < 8) ? out.vprime : out.kcd;
+        const bool to_vp = warp < 8;
 #pragma unroll
         for (int pass = 0; pass < 2; ++pass) {
             const int mt = (u < 4) ? (pass ? 3 : 0) : (pass ? 2 : 1);
-            float acc[4][4];
+            float acc3[4][3][4];
 #pragma unroll
             for (int n = 0; n < 4; ++n)
 #pragma unroll
-                for (int r = 0; r < 4; ++r) acc[n][r] = 0.f;
+                for (int r = 0; r < 12; ++r) acc3[n][r >> 2][r & 3] = 0.f;
             for (int k0 = 0; k0 < 16 * (mt + 1); k0 += 8) {
                 uint32_t ah[4], al[4];
                 load_a_split(sx, CL_LDA, mt * 16, k0, ah, al);
@@ -451,14 +479,23 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
                     uint32_t bh0, bl0, bh1, bl1;
                     tf32_split(br[0], bh0, bl0);
                     tf32_split(br[4 * CL_LDB], bh1, bl1);
-                    mma_3xtf32(acc[n], ah, al, bh0, bh1, bl0, bl1);
+                    mma_3xtf32_terms(acc3[n], ah, al, bh0, bh1, bl0, bl1);
                 }
             }
+            float acc[4][4];
+#pragma unroll
+            for (int n = 0; n < 4; ++n)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) acc[n][r] = sum_terms(acc3[n], r);
 #pragma unroll
             for (int n = 0; n < 4; ++n)
 #pragma unroll
                 for (int hr = 0; hr < 2; ++hr)
-                    *reinterpret_cast<float2*>(&dst[mt * 16 + gq + 8 * hr][nq * 32 + n * 8 + 2 * t4]) = make_float2(acc[n][2 * hr], acc[n][2 * hr + 1]);
+                {
+                    const int i = mt * 16 + gq + 8 * hr, d = nq * 32 + n * 8 + 2 * t4;
+                    float* dst = to_vp ? &out.vprime[d / SCAN_VW][i][d % SCAN_VW] : &out.kcd[i][d];
+                    *reinterpret_cast<float2*>(dst) = make_float2(acc[n][2 * hr], acc[n][2 * hr + 1]);
+                }
         }
     }
 }
@@ -472,23 +509,26 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
 //   P3  all warps: S' = S exp(gc_last) + ks^T v_new       (128 x 64 x 16, one 16-row tile per warp)
 // The state slice lives in registers as the f32 accumulator fragment of P3 from chunk to chunk (no precision is lost to
 // the operand split); shared memory holds its hi / lo split as the B operand of the next chunk's P1, and v_new likewise.
-// The left operands are plain copies of what the chunk-local kernel wrote and arrive by cp.async while the previous phase
-// computes: group 1 = {kcd, qs, vprime slice}, group 2 = {aqk, ks}, each refilled as soon as its buffers are free.
-constexpr int SCAN_VW = 16;
-constexpr int SCAN_THREADS = 256;
-constexpr int SCAN_LDA = DN_K + 4;          // kcd, qs: row-major A operands, bank = 4 g + t
-constexpr int SCAN_LDT = DN_K + 8;          // ks: read as its transpose, bank = 8 t + g
-constexpr int SCAN_LDQ = DN_CHUNK + 4;      // aqk
+// The left operands are plain copies of what the chunk-local kernel wrote, in the layout it wrote them.  A ninth warp brings
+// them in with five bulk copies per chunk (completion counted on an mbarrier): group 1 = {kcd, qs, vprime slice}, group 2 =
+// {ks, aqk}, each refilled as soon as the eight compute warps have released its buffers; no compute warp issues a copy.
+constexpr int SCAN_CONS = 256;              // compute threads
+constexpr int SCAN_THREADS = SCAN_CONS + 32;
 constexpr int SCAN_LDB = SCAN_VW + 8;       // B operands (state and v_new, hi and lo): bank = 24 t + g
 constexpr int CHUNK_SCAN_SMEM = (2 * DN_CHUNK * SCAN_LDA + DN_CHUNK * SCAN_LDT + DN_CHUNK * SCAN_LDQ + DN_CHUNK * SCAN_VW +
-                                 2 * DN_K * SCAN_LDB + 2 * DN_CHUNK * SCAN_LDB) * 4;
+                                 2 * DN_K * SCAN_LDB + 2 * DN_CHUNK * SCAN_LDB) * 4 + 64;
+constexpr uint32_t SCAN_G1_BYTES = DN_CHUNK * (2 * SCAN_LDA + SCAN_VW) * 4, SCAN_G2_BYTES = DN_CHUNK * (SCAN_LDT + SCAN_LDQ) * 4;
+constexpr unsigned SCAN_WAIT_LIMIT = 1u << 26;      // a bounded wait: a copy that never lands ends the loop instead of hanging
 
-__device__ __forceinline__ void scan_cp16(float* dst, const float* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src) : "memory");
+__device__ __forceinline__ void scan_wait(uint32_t bar, uint32_t parity, int* err) {
+    unsigned it = 0;
+    while (!mbar_try_wait(bar, parity))
+        if (++it >= SCAN_WAIT_LIMIT) { atomicCAS(err, 0, (int)ERR_BARRIER_TIMEOUT); return; }
 }
+__device__ __forceinline__ void scan_cons_sync() { asm volatile("bar.sync 1, %0;" ::"n"(SCAN_CONS) : "memory"); }
 
 static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(const ChunkScratch* __restrict__ scratch, bf16* __restrict__ core_out,
-                                                                        float* __restrict__ state_out, int S, int nchunks) {
+                                                                        float* __restrict__ state_out, int S, int nchunks, int* __restrict__ err) {
     pdl_wait();
     extern __shared__ __align__(16) float sm[];
     float* skcd = sm;                                   // [64][SCAN_LDA]
@@ -500,42 +540,37 @@ static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(c
     uint32_t* stl = sth + DN_K * SCAN_LDB;                                   //                  state, tf32 lo
     uint32_t* vnh = stl + DN_K * SCAN_LDB;                                   // [64][SCAN_LDB]  v_new, tf32 hi
     uint32_t* vnl = vnh + DN_CHUNK * SCAN_LDB;                               //                  v_new, tf32 lo
+    u64* bars = reinterpret_cast<u64*>(vnl + DN_CHUNK * SCAN_LDB);           // full1, full2, empty1, empty2
     const int h = blockIdx.x, vs = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t4 = lane & 3;
     const int v0 = vs * SCAN_VW;
+    const uint32_t full1 = smem_u32(bars), full2 = smem_u32(bars + 1), empty1 = smem_u32(bars + 2), empty2 = smem_u32(bars + 3);
+    if (tid == 0) {
+        mbar_init(full1, 1); mbar_init(full2, 1);
+        mbar_init(empty1, SCAN_CONS / 32); mbar_init(empty2, SCAN_CONS / 32);     // one arrival per compute warp
+        mbar_fence_init();
+    }
     for (int e = tid; e < 2 * DN_K * SCAN_LDB; e += SCAN_THREADS) sth[e] = 0u;          // state = 0 (hi and lo)
+    __syncthreads();
 
-    auto issue_g1 = [&](int c) {
-        if (c < nchunks) {
+    if (warp == SCAN_CONS / 32) {
+        // ---- producer warp (one lane issues) ----
+        for (int c = 0; c < nchunks; ++c) {
             const ChunkScratch& in = scratch[(size_t)h * nchunks + c];
-            for (int e = tid; e < DN_CHUNK * (DN_K / 4); e += SCAN_THREADS) {
-                const int i = e >> 5, q4 = (e & 31) * 4;
-                scan_cp16(skcd + i * SCAN_LDA + q4, &in.kcd[i][q4]);
-                scan_cp16(sq + i * SCAN_LDA + q4, &in.qs[i][q4]);
-            }
-            for (int e = tid; e < DN_CHUNK * (SCAN_VW / 4); e += SCAN_THREADS) {
-                const int i = e >> 2, q4 = (e & 3) * 4;
-                scan_cp16(svp + i * SCAN_VW + q4, &in.vprime[i][v0 + q4]);
+            if (lane == 0) {
+                if (c > 0) scan_wait(empty1, (c - 1) & 1, err);
+                mbar_arrive_expect_tx(full1, SCAN_G1_BYTES);
+                bulk_load_1d(smem_u32(skcd), &in.kcd[0][0], DN_CHUNK * SCAN_LDA * 4, full1);
+                bulk_load_1d(smem_u32(sq), &in.qs[0][0], DN_CHUNK * SCAN_LDA * 4, full1);
+                bulk_load_1d(smem_u32(svp), &in.vprime[vs][0][0], DN_CHUNK * SCAN_VW * 4, full1);
+                if (c > 0) scan_wait(empty2, (c - 1) & 1, err);
+                mbar_arrive_expect_tx(full2, SCAN_G2_BYTES);
+                bulk_load_1d(smem_u32(sk), &in.ks[0][0], DN_CHUNK * SCAN_LDT * 4, full2);
+                bulk_load_1d(smem_u32(sa), &in.aqk[0][0], DN_CHUNK * SCAN_LDQ * 4, full2);
             }
         }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-    };
-    auto issue_g2 = [&](int c) {
-        if (c < nchunks) {
-            const ChunkScratch& in = scratch[(size_t)h * nchunks + c];
-            for (int e = tid; e < DN_CHUNK * (DN_K / 4); e += SCAN_THREADS) {
-                const int i = e >> 5, q4 = (e & 31) * 4;
-                scan_cp16(sk + i * SCAN_LDT + q4, &in.ks[i][q4]);
-            }
-            for (int e = tid; e < DN_CHUNK * (DN_CHUNK / 4); e += SCAN_THREADS) {
-                const int i = e >> 4, q4 = (e & 15) * 4;
-                scan_cp16(sa + i * SCAN_LDQ + q4, &in.aqk[i][q4]);
-            }
-        }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-    };
-    issue_g1(0);
-    issue_g2(0);
+        return;
+    }
 
     // this warp's 16 x 16 piece of the state (rows = keys 16 warp .., columns = the slice's 16 values), f32, in registers
     float st[2][4];
@@ -547,27 +582,34 @@ static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(c
     for (int c = 0; c < nchunks; ++c) {
         const int t0 = c * DN_CHUNK;
         const float dec = scratch[(size_t)h * nchunks + c].eg_last[0];
-        asm volatile("cp.async.wait_group 1;" ::: "memory");          // group 1 of this chunk has landed
-        __syncthreads();                                               // ... for everybody; the state split of the previous chunk is complete
+        scan_wait(full1, c & 1, err);                                       // group 1 of this chunk has landed
         // ---- P1: VP = kcd S (warps 0-3), IT = qs S (warps 4-7) ----
         const int mt = warp & 3, m0 = mt * 16;
         float acc[2][4];
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-            for (int r = 0; r < 4; ++r) acc[nt][r] = 0.f;
         {
-            const float* A = (warp < 4) ? skcd : sq;
-#pragma unroll 4
-            for (int k0 = 0; k0 < DN_K; k0 += 8) {
-                uint32_t ah[4], al[4];
-                load_a_split(A, SCAN_LDA, m0, k0, ah, al);
+            // two halves of the k range x three terms: six independent accumulator chains per column tile
+            float a3[2][2][3][4];
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
-                    const int bi0 = (k0 + t4) * SCAN_LDB + nt * 8 + g, bi1 = bi0 + 4 * SCAN_LDB;
-                    mma_3xtf32(acc[nt], ah, al, sth[bi0], sth[bi1], stl[bi0], stl[bi1]);
+            for (int i = 0; i < 48; ++i) a3[i / 24][(i / 12) & 1][(i >> 2) % 3][i & 3] = 0.f;
+            const float* A = (warp < 4) ? skcd : sq;
+#pragma unroll 2
+            for (int k0 = 0; k0 < DN_K / 2; k0 += 8) {
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    const int kk = k0 + hf * (DN_K / 2);
+                    uint32_t ah[4], al[4];
+                    load_a_split(A, SCAN_LDA, m0, kk, ah, al);
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt) {
+                        const int bi0 = (kk + t4) * SCAN_LDB + nt * 8 + g, bi1 = bi0 + 4 * SCAN_LDB;
+                        mma_3xtf32_terms(a3[hf][nt], ah, al, sth[bi0], sth[bi1], stl[bi0], stl[bi1]);
+                    }
                 }
             }
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) acc[nt][r] = sum_terms(a3[0][nt], r) + sum_terms(a3[1][nt], r);
         }
         if (warp < 4) {
             // v_new = vprime - VP, stored split as the B operand of P2 and P3
@@ -582,21 +624,28 @@ static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(c
                     vnl[row * SCAN_LDB + col] = lo;
                 }
         }
-        __syncthreads();                                               // v_new complete; kcd / qs / vprime buffers are free
-        issue_g1(c + 1);
-        asm volatile("cp.async.wait_group 1;" ::: "memory");          // group 2 of this chunk has landed
-        __syncthreads();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty1, 1);                         // this warp is done with kcd / qs / vprime
+        scan_cons_sync();                                              // v_new complete
+        scan_wait(full2, c & 1, err);                                       // group 2 of this chunk has landed
         // ---- P2 (warps 4-7): out = IT + aqk v_new; aqk is lower triangular, so row tile mt needs tokens j < 16 (mt + 1) only ----
         if (warp >= 4) {
+            float a3[2][3][4];
+#pragma unroll
+            for (int i = 0; i < 24; ++i) a3[i / 12][(i >> 2) % 3][i & 3] = 0.f;
             for (int k0 = 0; k0 < 16 * (mt + 1); k0 += 8) {
                 uint32_t ah[4], al[4];
                 load_a_split(sa, SCAN_LDQ, m0, k0, ah, al);
 #pragma unroll
                 for (int nt = 0; nt < 2; ++nt) {
                     const int bi0 = (k0 + t4) * SCAN_LDB + nt * 8 + g, bi1 = bi0 + 4 * SCAN_LDB;
-                    mma_3xtf32(acc[nt], ah, al, vnh[bi0], vnh[bi1], vnl[bi0], vnl[bi1]);
+                    mma_3xtf32_terms(a3[nt], ah, al, vnh[bi0], vnh[bi1], vnl[bi0], vnl[bi1]);
                 }
             }
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) acc[nt][r] += sum_terms(a3[nt], r);
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
@@ -611,20 +660,27 @@ static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(c
         // ---- P3 (all warps): S' = S exp(gc_last) + ks^T v_new; this warp owns state rows (keys) 16 warp .. 16 warp + 15 ----
         {
             const int d0 = warp * 16;
+            float a3[2][2][3][4];
+#pragma unroll
+            for (int i = 0; i < 48; ++i) a3[i / 24][(i / 12) & 1][(i >> 2) % 3][i & 3] = 0.f;
+#pragma unroll 2
+            for (int k0 = 0; k0 < DN_CHUNK / 2; k0 += 8) {
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    const int kk = k0 + hf * (DN_CHUNK / 2);
+                    uint32_t ah[4], al[4];
+                    load_at_split(sk, SCAN_LDT, d0, kk, ah, al);
+#pragma unroll
+                    for (int nt = 0; nt < 2; ++nt) {
+                        const int bi0 = (kk + t4) * SCAN_LDB + nt * 8 + g, bi1 = bi0 + 4 * SCAN_LDB;
+                        mma_3xtf32_terms(a3[hf][nt], ah, al, vnh[bi0], vnh[bi1], vnl[bi0], vnl[bi1]);
+                    }
+                }
+            }
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-                for (int r = 0; r < 4; ++r) st[nt][r] *= dec;
-#pragma unroll 4
-            for (int k0 = 0; k0 < DN_CHUNK; k0 += 8) {
-                uint32_t ah[4], al[4];
-                load_at_split(sk, SCAN_LDT, d0, k0, ah, al);
-#pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
-                    const int bi0 = (k0 + t4) * SCAN_LDB + nt * 8 + g, bi1 = bi0 + 4 * SCAN_LDB;
-                    mma_3xtf32(st[nt], ah, al, vnh[bi0], vnh[bi1], vnl[bi0], vnl[bi1]);
-                }
-            }
+                for (int r = 0; r < 4; ++r) st[nt][r] = fmaf(st[nt][r], dec, sum_terms(a3[0][nt], r) + sum_terms(a3[1][nt], r));
             // the new state, split, for the next chunk's P1 (only this warp reads or writes these rows before the barrier)
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt)
@@ -637,10 +693,10 @@ static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(c
                     stl[row * SCAN_LDB + col] = lo;
                 }
         }
-        __syncthreads();                                               // aqk / ks / v_new buffers are free
-        issue_g2(c + 1);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty2, 1);                         // this warp is done with aqk / ks
+        scan_cons_sync();                                              // the new state split is complete; v_new may be overwritten
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
     // final state in the reference layout [head][v][k], from the f32 registers
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
