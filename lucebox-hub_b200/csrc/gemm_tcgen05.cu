@@ -29,9 +29,16 @@ constexpr int GEMM_BM = 128, GEMM_BN = 128, GEMM_BK = 64;
 constexpr int GEMM_THREADS = 192;
 constexpr uint32_t GEMM_STAGE_BYTES = (GEMM_BM + GEMM_BN) * GEMM_BK * 2;   // 32 KB
 // 6 stages for the wide problems (one CTA per SM); the skinny ones run a few k-steps per CTA: 3 stages, two CTAs per SM
-constexpr int GEMM_STAGES_WIDE = 6, GEMM_STAGES_SKINNY = 3;
-__host__ __device__ constexpr uint32_t gemm_smem(int stages) { return stages * GEMM_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/; }
-static_assert(GEMM_STAGES_SKINNY * GEMM_STAGE_BYTES >= GEMM_BM * GEMM_BN * 4, "the parked f32 tile reuses the stage buffers");
+constexpr int GEMM_STAGES_WIDE = 6, GEMM_STAGES_SKINNY = 3, GEMM_STAGES_THIRD = 2;     // one, two, three CTAs per SM
+// The epilogue parks the f32 accumulator tile in the (then idle) stage buffers as [row][GEMM_PARK_LD]: with a pitch of
+// 132 floats the float4 accesses of eight adjacent rows (writing, one row per thread) and of one row's adjacent column
+// groups (reading) both spread over all 32 banks.
+constexpr int GEMM_PARK_LD = GEMM_BN + 4;
+constexpr uint32_t GEMM_PARK_BYTES = GEMM_BM * GEMM_PARK_LD * 4;
+__host__ __device__ constexpr uint32_t gemm_tile_bytes(int stages) {
+    return stages * GEMM_STAGE_BYTES > GEMM_PARK_BYTES ? stages * GEMM_STAGE_BYTES : ((GEMM_PARK_BYTES + 1023u) & ~1023u);
+}
+__host__ __device__ constexpr uint32_t gemm_smem(int stages) { return gemm_tile_bytes(stages) + 1024 /*align*/ + 256 /*barriers*/; }
 constexpr int GEMM_MAX_SPLIT = 8;        // portable cluster size
 constexpr unsigned GEMM_SPIN_LIMIT = 20u * 1000u * 1000u;
 enum GemmEpi { EPI_BF16 = 0, EPI_RESIDUAL = 1, EPI_SILU_MUL = 2 };
@@ -208,16 +215,114 @@ __device__ __forceinline__ void cluster_reduce_store(const GemmParams& p, uint32
     }
 }
 
+__device__ __forceinline__ float4 ld_dsmem4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ float4 ld_smem4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
+    return v;
+}
+
+// Store pass of the tcgen05 bf16 GEMM over the parked tile(s) [row][GEMM_PARK_LD].  A work item is one row x 8 adjacent
+// output columns; consecutive threads take consecutive column groups of a row, so the 16-byte stores (and residual loads) of
+// a warp cover whole row segments.  With S > 1 every CTA of the cluster has parked its partial tile at the same
+// shared-memory offset; CTA `rank` finishes a contiguous range of column groups, requests all peers' values before it uses
+// the first (one remote round trip, not S) and sums them in peer order, so the result does not depend on timing.
+template <int EPI>
+__device__ __forceinline__ void parked_tile_store(const GemmParams& p, uint32_t park_local, int S, int rank, int rows, int m0, int n0, int t, int nt) {
+    constexpr int BN_OUT = (EPI == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
+    constexpr int NG = BN_OUT / 8;
+    constexpr int UNR = 4;                                   // rows in flight per thread: their loads are all issued before the first is used
+    const int g_begin = rank * NG / S, g_cnt = (rank + 1) * NG / S - g_begin;     // S is a power of two <= 8: g_cnt divides nt
+    const int col = (g_begin + t % g_cnt) * 8, r_first = t / g_cnt, r_step = nt / g_cnt;
+    uint32_t base[GEMM_MAX_SPLIT];
+#pragma unroll
+    for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer) base[peer] = (S > 1 && peer < S) ? map_to_cta(park_local, (uint32_t)peer) : park_local;
+    // the fast path of the residual: whole 16-byte groups inside N, both pointers 16-byte aligned for every row
+    const bool vec_ok = n0 + col + 8 <= p.N && ((reinterpret_cast<uintptr_t>(p.C + n0 + col) | (size_t)p.ldc * 2) & 15) == 0 &&
+                        (EPI != EPI_RESIDUAL || ((reinterpret_cast<uintptr_t>(p.R + n0 + col) | (size_t)p.ldr * 2) & 15) == 0);
+    for (int rb = r_first; rb < rows; rb += UNR * r_step) {
+        float g[UNR][8], u[UNR][8];
+        uint4 res[UNR];
+#pragma unroll
+        for (int q = 0; q < UNR; ++q) {
+            const int r = rb + q * r_step;
+            res[q] = make_uint4(0u, 0u, 0u, 0u);
+            if (EPI == EPI_RESIDUAL && vec_ok && r < rows) res[q] = *reinterpret_cast<const uint4*>(p.R + (size_t)(m0 + r) * p.ldr + n0 + col);
+        }
+#pragma unroll
+        for (int q = 0; q < UNR; ++q) {
+            const int r = min(rb + q * r_step, rows - 1);
+            const uint32_t off = (uint32_t)((r * GEMM_PARK_LD + col) * 4);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) { g[q][e] = 0.f; u[q][e] = 0.f; }
+            if (S == 1) {
+                const float4 a = ld_smem4(park_local + off), b = ld_smem4(park_local + off + 16);
+                g[q][0] = a.x; g[q][1] = a.y; g[q][2] = a.z; g[q][3] = a.w; g[q][4] = b.x; g[q][5] = b.y; g[q][6] = b.z; g[q][7] = b.w;
+                if (EPI == EPI_SILU_MUL) {
+                    const float4 c = ld_smem4(park_local + off + 256), d = ld_smem4(park_local + off + 272);
+                    u[q][0] = c.x; u[q][1] = c.y; u[q][2] = c.z; u[q][3] = c.w; u[q][4] = d.x; u[q][5] = d.y; u[q][6] = d.z; u[q][7] = d.w;
+                }
+            } else {
+                float4 v[GEMM_MAX_SPLIT][2];
+#pragma unroll
+                for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
+                    if (peer < S) { v[peer][0] = ld_dsmem4(base[peer] + off); v[peer][1] = ld_dsmem4(base[peer] + off + 16); }
+#pragma unroll
+                for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
+                    if (peer < S) {
+                        g[q][0] += v[peer][0].x; g[q][1] += v[peer][0].y; g[q][2] += v[peer][0].z; g[q][3] += v[peer][0].w;
+                        g[q][4] += v[peer][1].x; g[q][5] += v[peer][1].y; g[q][6] += v[peer][1].z; g[q][7] += v[peer][1].w;
+                    }
+                if (EPI == EPI_SILU_MUL) {
+#pragma unroll
+                    for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
+                        if (peer < S) { v[peer][0] = ld_dsmem4(base[peer] + off + 256); v[peer][1] = ld_dsmem4(base[peer] + off + 272); }
+#pragma unroll
+                    for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
+                        if (peer < S) {
+                            u[q][0] += v[peer][0].x; u[q][1] += v[peer][0].y; u[q][2] += v[peer][0].z; u[q][3] += v[peer][0].w;
+                            u[q][4] += v[peer][1].x; u[q][5] += v[peer][1].y; u[q][6] += v[peer][1].z; u[q][7] += v[peer][1].w;
+                        }
+                }
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < UNR; ++q) {
+            const int r = rb + q * r_step;
+            if (r >= rows) break;
+            if (!vec_ok) { epilogue_store8<EPI>(p, m0 + r, n0 + col, g[q], u[q]); continue; }
+            float y[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) y[j] = (EPI == EPI_SILU_MUL) ? rbf(silu_f(rbf(g[q][j]))) * rbf(u[q][j]) : rbf(g[q][j]);
+            if (EPI == EPI_RESIDUAL) {
+                y[0] += bf_lo(res[q].x); y[1] += bf_hi(res[q].x); y[2] += bf_lo(res[q].y); y[3] += bf_hi(res[q].y);
+                y[4] += bf_lo(res[q].z); y[5] += bf_hi(res[q].z); y[6] += bf_lo(res[q].w); y[7] += bf_hi(res[q].w);
+            }
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const __nv_bfloat162 pr = __halves2bfloat162(f2bf(y[2 * j]), f2bf(y[2 * j + 1]));
+                o[j] = *reinterpret_cast<const uint32_t*>(&pr);
+            }
+            *reinterpret_cast<uint4*>(p.C + (size_t)(m0 + r) * p.ldc + n0 + col) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    }
+}
+
 // SPLIT: gridDim.z = cluster size S along K (1, 2, 4 or 8); the cluster shares one output tile
 template <int EPI, int STAGES, bool SPLIT>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __launch_bounds__(GEMM_THREADS, STAGES == GEMM_STAGES_THIRD ? 3 : (STAGES == GEMM_STAGES_SKINNY ? 2 : 1))
 gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
     extern __shared__ unsigned char g_smem_raw[];
     // 128B-swizzled tiles need 1024-byte alignment
     const uint32_t raw = g_smem_u32(g_smem_raw);
     const uint32_t tiles = (raw + 1023u) & ~1023u;
     unsigned char* tiles_ptr = g_smem_raw + (tiles - raw);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(tiles_ptr + STAGES * GEMM_STAGE_BYTES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(tiles_ptr + gemm_tile_bytes(STAGES));
     const uint32_t full0 = g_smem_u32(bars), empty0 = full0 + 8 * STAGES, tfull = empty0 + 8 * STAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
     volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -289,49 +394,35 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
     } else {
         // ---- epilogue: warp w may touch TMEM lanes [32*(w%4), +32) ----
         const int q = warp & 3;
-        const int rloc = q * 32 + lane, row = m0 + rloc;
+        const int rloc = q * 32 + lane;
         // warp-uniform, because tcgen05.ld is a warp-wide instruction
         const bool ok = __all_sync(0xffffffffu, g_mbar_wait(tfull, 0, p.err, s_abort) && !*s_abort);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        if (SPLIT) {
-            // park the f32 tile column-major in the (now idle) stage buffers: [column][row], conflict-free for a warp
-            float* park = reinterpret_cast<float*>(tiles_ptr);
+        // park the f32 tile in the (now idle) stage buffers, one row per thread
+        float* park = reinterpret_cast<float*>(tiles_ptr);
+        if (m0 + q * 32 < p.M) {                                // else: rows of this warp are never read back
 #pragma unroll
             for (int c = 0; c < GEMM_BN / 32; ++c) {
-                if (m0 + q * 32 >= p.M) break;                  // rows of this warp are never read back
                 uint32_t v[32];
                 if (ok) {
                     tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 }
 #pragma unroll
-                for (int j = 0; j < 32; ++j) park[(c * 32 + j) * GEMM_BM + rloc] = ok ? __uint_as_float(v[j]) : 0.f;
-            }
-        } else if (ok) {
-#pragma unroll
-            for (int c = 0; c < BN_OUT / 32; ++c) {
-                uint32_t g[32], u[32];
-                tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), g);
-                if (EPI == EPI_SILU_MUL) tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(64 + c * 32), u);
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (row < p.M) {
-#pragma unroll
-                    for (int j = 0; j < 32; j += 8) {
-                        float gf[8], uf[8];
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) { gf[e] = __uint_as_float(g[j + e]); uf[e] = (EPI == EPI_SILU_MUL) ? __uint_as_float(u[j + e]) : 0.f; }
-                        epilogue_store8<EPI>(p, row, n0 + c * 32 + j, gf, uf);
-                    }
-                }
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4*>(park + rloc * GEMM_PARK_LD + c * 32 + j) =
+                        ok ? make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
             }
         }
     }
+    // The store pass is arithmetic and address work on shared memory: all six warps take part (the copy and MMA warps are
+    // idle by now).  Every thread of every CTA of a cluster passes both barriers, whatever happened above.
+    __syncwarp();
+    if (SPLIT) cluster_sync_all(); else __syncthreads();
+    if (!*s_abort)
+        parked_tile_store<EPI>(p, tiles, S, SPLIT ? (int)cluster_ctarank() : 0, min(GEMM_BM, p.M - m0), m0, n0, (int)threadIdx.x, GEMM_THREADS);
     if (SPLIT) {
-        // every thread of every CTA of the cluster passes both barriers, whatever happened above
-        __syncwarp();
-        cluster_sync_all();
-        if (warp >= 2 && !*s_abort)
-            cluster_reduce_store<EPI>(p, tiles, S, min(GEMM_BM, p.M - m0), m0, n0, (int)threadIdx.x - 64, GEMM_THREADS - 64);
         __syncwarp();
         cluster_sync_all();                                     // no CTA leaves while a peer may still read its tile
     }
@@ -652,6 +743,25 @@ static cudaError_t gemm_launch(K kernel, dim3 grid, size_t smem, cudaStream_t st
     return cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, p);
 }
 
+template <int E, int ST>
+static int gemm_plain(dim3 grid, cudaStream_t stream, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p) {
+    static PerDeviceOnce attr;
+    if (attr.pending()) {
+        Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<E, ST, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem(ST)));
+        attr.mark();
+    }
+    Q35_CUDA_OK(gemm_launch(gemm_bf16_tcgen05_kernel<E, ST, false>, grid, gemm_smem(ST), stream, tmA, tmB, p));
+    return QWEN35_OK;
+}
+template <int ST>
+static int gemm_plain_epi(int epi, dim3 grid, cudaStream_t stream, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p) {
+    switch (epi) {
+        case EPI_BF16: return gemm_plain<EPI_BF16, ST>(grid, stream, tmA, tmB, p);
+        case EPI_RESIDUAL: return gemm_plain<EPI_RESIDUAL, ST>(grid, stream, tmA, tmB, p);
+        default: return gemm_plain<EPI_SILU_MUL, ST>(grid, stream, tmA, tmB, p);
+    }
+}
+
 // C[M,N] (row stride ldc) = epi(A[M,K] (row stride lda) . B[*,K]^T).  epi: 0 bf16, 1 + R, 2 silu(gate)*up with
 // gate rows [0,N) and up rows [up_row_offset, up_row_offset+N) of B.  b_rows = number of rows of B.
 int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ldc, const bf16* R, int ldr,
@@ -674,58 +784,25 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
     const int m_tiles = (M + GEMM_BM - 1) / GEMM_BM, n_tiles = (N + bn_out - 1) / bn_out, nkb = K / GEMM_BK;
     // a grid that cannot fill the SMs (few tiles, long K) also splits K over clusters
     const bool small_grid = m_tiles * n_tiles < 100 && nkb >= 8;
-    // more tiles than SMs: 3 stages per CTA let two CTAs share an SM (the same bytes in flight per SM as 6 stages of one
-    // CTA), so the prologue / epilogue of one tile overlaps the main loop of another
-    const bool two_per_sm = m_tiles > 1 && !small_grid && m_tiles * n_tiles > 148;
-    if (two_per_sm) {
-        dim3 grid(n_tiles, m_tiles);
-#define Q35_GEMM_ROW2(E)                                                                                                                        \
-    case E: {                                                                                                                                   \
-        static PerDeviceOnce attr;                                                                                                               \
-        if (attr.pending()) {                                                                                                                            \
-            Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                             (int)gemm_smem(GEMM_STAGES_SKINNY)));                                                              \
-            attr.mark();                                                                                                                        \
-        }                                                                                                                                       \
-        Q35_CUDA_OK(gemm_launch(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, false>, grid, gemm_smem(GEMM_STAGES_SKINNY), stream, tmA, tmB, p));      \
-        break;                                                                                                                                  \
-    }
-        switch (epi) { Q35_GEMM_ROW2(EPI_BF16) Q35_GEMM_ROW2(EPI_RESIDUAL) Q35_GEMM_ROW2(EPI_SILU_MUL) }
-#undef Q35_GEMM_ROW2
-    } else if (m_tiles > 1 && !small_grid) {
-        dim3 grid(n_tiles, m_tiles);
-#define Q35_GEMM_WIDE(E)                                                                                                                      \
-    case E: {                                                                                                                                 \
-        static PerDeviceOnce attr;                                                                                                             \
-        if (attr.pending()) {                                                                                                                          \
-            Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_WIDE, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                             (int)gemm_smem(GEMM_STAGES_WIDE)));                                                              \
-            attr.mark();                                                                                                                      \
-        }                                                                                                                                     \
-        Q35_CUDA_OK(gemm_launch(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_WIDE, false>, grid, gemm_smem(GEMM_STAGES_WIDE), stream, tmA, tmB, p));        \
-        break;                                                                                                                                \
-    }
-        switch (epi) { Q35_GEMM_WIDE(EPI_BF16) Q35_GEMM_WIDE(EPI_RESIDUAL) Q35_GEMM_WIDE(EPI_SILU_MUL) }
-#undef Q35_GEMM_WIDE
+    const int tiles_total = m_tiles * n_tiles;
+    if (m_tiles > 1 && !small_grid) {
+        // One CTA per SM with six stages while the tiles fit one wave; more tiles than SMs: three (two) stages per CTA let
+        // two (three) CTAs share an SM -- the same bytes in flight per SM -- so that the prologue and epilogue of one tile
+        // overlap the main loop of another and a tile count a little above a multiple of 148 does not leave a second wave
+        // nearly empty.  Beyond three waves' worth of tiles the two-per-SM form is used.
+        const dim3 grid(n_tiles, m_tiles);
+        int st;
+        if (tiles_total <= 148) st = gemm_plain_epi<GEMM_STAGES_WIDE>(epi, grid, stream, tmA, tmB, p);
+        else if (tiles_total > 296 && tiles_total <= 444) st = gemm_plain_epi<GEMM_STAGES_THIRD>(epi, grid, stream, tmA, tmB, p);
+        else st = gemm_plain_epi<GEMM_STAGES_SKINNY>(epi, grid, stream, tmA, tmB, p);
+        if (st != QWEN35_OK) return st;
     } else {
         // few tiles: split K over a cluster until about one CTA per SM exists, at least two k-steps per CTA
         int split = 1;
         while (split < GEMM_MAX_SPLIT && m_tiles * n_tiles * split < 120 && nkb / (split * 2) >= 2) split *= 2;
         if (split == 1) {
-            dim3 grid(n_tiles, m_tiles);
-#define Q35_GEMM_ROW(E)                                                                                                                         \
-    case E: {                                                                                                                                   \
-        static PerDeviceOnce attr;                                                                                                               \
-        if (attr.pending()) {                                                                                                                            \
-            Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                             (int)gemm_smem(GEMM_STAGES_SKINNY)));                                                              \
-            attr.mark();                                                                                                                        \
-        }                                                                                                                                       \
-        Q35_CUDA_OK(gemm_launch(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, false>, grid, gemm_smem(GEMM_STAGES_SKINNY), stream, tmA, tmB, p));      \
-        break;                                                                                                                                  \
-    }
-            switch (epi) { Q35_GEMM_ROW(EPI_BF16) Q35_GEMM_ROW(EPI_RESIDUAL) Q35_GEMM_ROW(EPI_SILU_MUL) }
-#undef Q35_GEMM_ROW
+            const int st = gemm_plain_epi<GEMM_STAGES_SKINNY>(epi, dim3(n_tiles, m_tiles), stream, tmA, tmB, p);
+            if (st != QWEN35_OK) return st;
             Q35_CUDA_OK(cudaGetLastError());
             g_launches.fetch_add(1);
             return QWEN35_OK;
