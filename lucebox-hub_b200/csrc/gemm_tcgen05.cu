@@ -2,13 +2,15 @@
 // projections:  C[M,N] = A[M,K] . B[N,K]^T  with f32 accumulation in tensor memory.
 //
 // Replaces the cuBLAS calls of the reference's prefill (cublas_bf16_gemm, prefill.cu:895-903 and its
-// ten call sites :1267-1434).  One CTA computes one 128 x BN output tile (BN = 128, 64, 32 or 16: the narrow
-// tiles spread a skinny problem, M <= 128 rows of activations against a tall weight matrix, over all SMs):
+// ten call sites :1267-1434).  One CTA computes one 128 x 128 output tile:
 //   warp 0     TMA producer: 128B-swizzled 64-wide K slices of A and B into a ring of stages
-//   warp 1     allocates the TMEM columns, then one thread issues tcgen05.mma (M128 N=BN K16 x4 per
+//   warp 1     allocates the TMEM columns, then one thread issues tcgen05.mma (M128 N128 K16 x4 per
 //              stage) and commits each stage back to the producer
-//   warps 2-5  epilogue: tcgen05.ld the accumulator rows, round once to bf16 (what a bf16 linear
-//              layer returns), optionally fuse the residual add or silu(gate)*up, store
+//   warps 2-5  tcgen05.ld the accumulator rows and park them as f32 in the idle stage buffers; then all six warps
+//              read the tile back as row segments, round once to bf16 (what a bf16 linear layer returns), optionally
+//              fuse the residual add or silu(gate)*up, and store 16 bytes per thread, a warp covering whole rows
+// Six, three or two stages per CTA put one, two or three CTAs on an SM (the same bytes in flight per SM), chosen by the
+// tile count so that no wave is left nearly empty and one tile's epilogue overlaps another's main loop.
 // A skinny problem (M <= 128 rows of activations against a tall weight matrix) is bound by the fixed cost of a
 // k-step (barrier hand-offs: about 0.3 us whatever the tile holds), not by bytes or flops, so it runs split along
 // K: a thread-block cluster of S CTAs shares one 128 x 128 output tile, each CTA accumulates its slice of K in
@@ -39,6 +41,7 @@ __host__ __device__ constexpr uint32_t gemm_tile_bytes(int stages) {
     return stages * GEMM_STAGE_BYTES > GEMM_PARK_BYTES ? stages * GEMM_STAGE_BYTES : ((GEMM_PARK_BYTES + 1023u) & ~1023u);
 }
 __host__ __device__ constexpr uint32_t gemm_smem(int stages) { return gemm_tile_bytes(stages) + 1024 /*align*/ + 256 /*barriers*/; }
+static_assert(GEMM_STAGES_SKINNY * GEMM_STAGE_BYTES >= GEMM_BM * GEMM_BN * 4, "the split-K form parks its f32 tile [column][row] in the stage buffers");
 constexpr int GEMM_MAX_SPLIT = 8;        // portable cluster size
 constexpr unsigned GEMM_SPIN_LIMIT = 20u * 1000u * 1000u;
 enum GemmEpi { EPI_BF16 = 0, EPI_RESIDUAL = 1, EPI_SILU_MUL = 2 };
@@ -215,33 +218,22 @@ __device__ __forceinline__ void cluster_reduce_store(const GemmParams& p, uint32
     }
 }
 
-__device__ __forceinline__ float4 ld_dsmem4(uint32_t addr) {
-    float4 v;
-    asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
-    return v;
-}
 __device__ __forceinline__ float4 ld_smem4(uint32_t addr) {
     float4 v;
     asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
     return v;
 }
 
-// Store pass of the tcgen05 bf16 GEMM over the parked tile(s) [row][GEMM_PARK_LD].  A work item is one row x 8 adjacent
+// Store pass of a one-CTA tile over its parked accumulator [row][GEMM_PARK_LD].  A work item is one row x 8 adjacent
 // output columns; consecutive threads take consecutive column groups of a row, so the 16-byte stores (and residual loads) of
-// a warp cover whole row segments.  With S > 1 every CTA of the cluster has parked its partial tile at the same
-// shared-memory offset; CTA `rank` finishes a contiguous range of column groups, requests all peers' values before it uses
-// the first (one remote round trip, not S) and sums them in peer order, so the result does not depend on timing.
+// a warp cover whole row segments.  Four rows are in flight per thread: their loads are all issued before the first is used.
 template <int EPI>
-__device__ __forceinline__ void parked_tile_store(const GemmParams& p, uint32_t park_local, int S, int rank, int rows, int m0, int n0, int t, int nt) {
+__device__ __forceinline__ void parked_tile_store(const GemmParams& p, uint32_t park_local, int rows, int m0, int n0, int t, int nt) {
     constexpr int BN_OUT = (EPI == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
     constexpr int NG = BN_OUT / 8;
-    constexpr int UNR = 4;                                   // rows in flight per thread: their loads are all issued before the first is used
-    const int g_begin = rank * NG / S, g_cnt = (rank + 1) * NG / S - g_begin;     // S is a power of two <= 8: g_cnt divides nt
-    const int col = (g_begin + t % g_cnt) * 8, r_first = t / g_cnt, r_step = nt / g_cnt;
-    uint32_t base[GEMM_MAX_SPLIT];
-#pragma unroll
-    for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer) base[peer] = (S > 1 && peer < S) ? map_to_cta(park_local, (uint32_t)peer) : park_local;
-    // the fast path of the residual: whole 16-byte groups inside N, both pointers 16-byte aligned for every row
+    constexpr int UNR = 4;
+    const int col = (t % NG) * 8, r_first = t / NG, r_step = nt / NG;
+    // the fast path: whole 16-byte groups inside N, both pointers 16-byte aligned for every row
     const bool vec_ok = n0 + col + 8 <= p.N && ((reinterpret_cast<uintptr_t>(p.C + n0 + col) | (size_t)p.ldc * 2) & 15) == 0 &&
                         (EPI != EPI_RESIDUAL || ((reinterpret_cast<uintptr_t>(p.R + n0 + col) | (size_t)p.ldr * 2) & 15) == 0);
     for (int rb = r_first; rb < rows; rb += UNR * r_step) {
@@ -257,37 +249,13 @@ __device__ __forceinline__ void parked_tile_store(const GemmParams& p, uint32_t 
         for (int q = 0; q < UNR; ++q) {
             const int r = min(rb + q * r_step, rows - 1);
             const uint32_t off = (uint32_t)((r * GEMM_PARK_LD + col) * 4);
+            const float4 a = ld_smem4(park_local + off), b = ld_smem4(park_local + off + 16);
+            g[q][0] = a.x; g[q][1] = a.y; g[q][2] = a.z; g[q][3] = a.w; g[q][4] = b.x; g[q][5] = b.y; g[q][6] = b.z; g[q][7] = b.w;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) { g[q][e] = 0.f; u[q][e] = 0.f; }
-            if (S == 1) {
-                const float4 a = ld_smem4(park_local + off), b = ld_smem4(park_local + off + 16);
-                g[q][0] = a.x; g[q][1] = a.y; g[q][2] = a.z; g[q][3] = a.w; g[q][4] = b.x; g[q][5] = b.y; g[q][6] = b.z; g[q][7] = b.w;
-                if (EPI == EPI_SILU_MUL) {
-                    const float4 c = ld_smem4(park_local + off + 256), d = ld_smem4(park_local + off + 272);
-                    u[q][0] = c.x; u[q][1] = c.y; u[q][2] = c.z; u[q][3] = c.w; u[q][4] = d.x; u[q][5] = d.y; u[q][6] = d.z; u[q][7] = d.w;
-                }
-            } else {
-                float4 v[GEMM_MAX_SPLIT][2];
-#pragma unroll
-                for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
-                    if (peer < S) { v[peer][0] = ld_dsmem4(base[peer] + off); v[peer][1] = ld_dsmem4(base[peer] + off + 16); }
-#pragma unroll
-                for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
-                    if (peer < S) {
-                        g[q][0] += v[peer][0].x; g[q][1] += v[peer][0].y; g[q][2] += v[peer][0].z; g[q][3] += v[peer][0].w;
-                        g[q][4] += v[peer][1].x; g[q][5] += v[peer][1].y; g[q][6] += v[peer][1].z; g[q][7] += v[peer][1].w;
-                    }
-                if (EPI == EPI_SILU_MUL) {
-#pragma unroll
-                    for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
-                        if (peer < S) { v[peer][0] = ld_dsmem4(base[peer] + off + 256); v[peer][1] = ld_dsmem4(base[peer] + off + 272); }
-#pragma unroll
-                    for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
-                        if (peer < S) {
-                            u[q][0] += v[peer][0].x; u[q][1] += v[peer][0].y; u[q][2] += v[peer][0].z; u[q][3] += v[peer][0].w;
-                            u[q][4] += v[peer][1].x; u[q][5] += v[peer][1].y; u[q][6] += v[peer][1].z; u[q][7] += v[peer][1].w;
-                        }
-                }
+            for (int e = 0; e < 8; ++e) u[q][e] = 0.f;
+            if (EPI == EPI_SILU_MUL) {
+                const float4 c = ld_smem4(park_local + off + 256), d = ld_smem4(park_local + off + 272);
+                u[q][0] = c.x; u[q][1] = c.y; u[q][2] = c.z; u[q][3] = c.w; u[q][4] = d.x; u[q][5] = d.y; u[q][6] = d.z; u[q][7] = d.w;
             }
         }
 #pragma unroll
@@ -398,7 +366,9 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
         // warp-uniform, because tcgen05.ld is a warp-wide instruction
         const bool ok = __all_sync(0xffffffffu, g_mbar_wait(tfull, 0, p.err, s_abort) && !*s_abort);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        // park the f32 tile in the (now idle) stage buffers, one row per thread
+        // park the f32 tile in the (now idle) stage buffers.  Split K: column-major [column][row], which makes the peers'
+        // reads through distributed shared memory whole 128-byte lines (measured faster there than 16-byte pieces of rows);
+        // one CTA per tile: row-major with a padded pitch, read back below as row segments.
         float* park = reinterpret_cast<float*>(tiles_ptr);
         if (m0 + q * 32 < p.M) {                                // else: rows of this warp are never read back
 #pragma unroll
@@ -408,23 +378,32 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
                     tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 }
+                if (SPLIT) {
 #pragma unroll
-                for (int j = 0; j < 32; j += 4)
-                    *reinterpret_cast<float4*>(park + rloc * GEMM_PARK_LD + c * 32 + j) =
-                        ok ? make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]))
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int j = 0; j < 32; ++j) park[(c * 32 + j) * GEMM_BM + rloc] = ok ? __uint_as_float(v[j]) : 0.f;
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4)
+                        *reinterpret_cast<float4*>(park + rloc * GEMM_PARK_LD + c * 32 + j) =
+                            ok ? make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
             }
         }
     }
-    // The store pass is arithmetic and address work on shared memory: all six warps take part (the copy and MMA warps are
-    // idle by now).  Every thread of every CTA of a cluster passes both barriers, whatever happened above.
     __syncwarp();
-    if (SPLIT) cluster_sync_all(); else __syncthreads();
-    if (!*s_abort)
-        parked_tile_store<EPI>(p, tiles, S, SPLIT ? (int)cluster_ctarank() : 0, min(GEMM_BM, p.M - m0), m0, n0, (int)threadIdx.x, GEMM_THREADS);
     if (SPLIT) {
+        // every thread of every CTA of the cluster passes both barriers, whatever happened above
+        cluster_sync_all();
+        if (warp >= 2 && !*s_abort)
+            cluster_reduce_store<EPI>(p, tiles, S, min(GEMM_BM, p.M - m0), m0, n0, (int)threadIdx.x - 64, GEMM_THREADS - 64);
         __syncwarp();
         cluster_sync_all();                                     // no CTA leaves while a peer may still read its tile
+    } else {
+        // the store pass is arithmetic and address work on shared memory: all six warps take part (the copy and MMA warps
+        // are idle by now)
+        __syncthreads();
+        if (!*s_abort) parked_tile_store<EPI>(p, tiles, min(GEMM_BM, p.M - m0), m0, n0, (int)threadIdx.x, GEMM_THREADS);
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();

@@ -7,6 +7,7 @@ sizes; the command line of this module runs ONE of them alone at a reduced size,
   python -m qwen35_b200.workloads draft_forward --iters 1
   python -m qwen35_b200.workloads prefill --lengths 512 --iters 1 [--nvfp4]
   python -m qwen35_b200.workloads decode --prompt 64 --gen 8
+  python -m qwen35_b200.workloads decode_stages            (per-stage time table of the decode megakernel)
   python -m qwen35_b200.workloads batched --batch 64 --ctx 256 --gen 4 --kernel-table
 """
 from __future__ import annotations
@@ -245,10 +246,47 @@ def decode_case(dev, prompt=64, gen=8, backend="bf16"):
     return {"prompt": prompt, "gen": gen, "backend": backend, "ms_per_token": e0.elapsed_time(e1) / gen, "tokens": toks.tolist()[:8]}
 
 
+def decode_stage_table(dev, ctx=520, gen=16):
+    """Per-stage time table of the bs=1 decode megakernel: the kernel records a clock64 stamp per CTA, layer and hand-off
+    (dbg_time of the decode entry point); reported are medians over the 148 CTAs and over the layers of a kind, in
+    microseconds at the 1965 MHz the kernel runs at, for the last of `gen` tokens decoded from a `ctx`-token position.
+    'X.in' = the stage's input vector has arrived, 'X.pub' = the CTA has published its part of the stage's output."""
+    import numpy as np
+    from qwen35_b200.config import QWEN35_0P8B as D
+    from qwen35_b200.model import Decoder
+    from qwen35_b200.weights import make_random_weights, weights_to
+    dec = Decoder(weights=weights_to(make_random_weights(1234, D), dev), max_seq_len=2048, device=dev)
+    dec.reset(); dec._position = ctx
+    for _ in range(2):
+        dec.step_many(5, gen)
+    dec.reset(); dec._position = ctx
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(); dec.step_many(5, 128); e1.record(); torch.cuda.synchronize(dev)
+    us_per_token = e0.elapsed_time(e1) * 1e3 / 128
+    dec.reset(); dec._position = ctx
+    tl = torch.zeros(148, 25, 12, dtype=torch.int64, device=dev)
+    dec.step_many(5, gen, dbg_time=tl, dbg_time_cta=-2)
+    torch.cuda.synchronize(dev)
+    dec.check_status()
+    t = tl.cpu().numpy().astype(np.float64) / 1965.0
+    names = ["start", "A.in", "A.pub", "B.pub", "C.in", "C.pub", "D.in", "D.pub", "E.in", "E.pub"]
+    out = {"us_per_token_untimed_run": us_per_token, "context": ctx}
+    for typ, tn in ((0, "deltanet"), (1, "attention")):
+        rows = [l for l in range(4, 24) if D.layer_types[l] == typ]
+        seg = {}
+        for a_, b_ in zip(range(9), range(1, 10)):
+            d = t[:, rows, b_] - t[:, rows, a_]
+            seg[f"{names[a_]}->{names[b_]}"] = round(float(np.median(d)), 2)
+        seg["layer"] = round(float(np.median(t[:, rows, 9] - t[:, rows, 0])), 2)
+        out[tn] = seg
+    out["lm_head"] = round(float(np.median(t[:, 24, 3] - t[:, 24, 0])), 2)
+    return out
+
+
 def main(argv=None):
     import argparse
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("case", choices=["tree_verify", "draft_forward", "prefill", "decode", "batched"])
+    ap.add_argument("case", choices=["tree_verify", "draft_forward", "prefill", "decode", "decode_stages", "batched"])
     ap.add_argument("--iters", type=int, default=1)
     ap.add_argument("--layers", type=int, default=4, help="tree_verify: layers of the 27B-width model (64 = the bench's)")
     ap.add_argument("--ctx", type=int, default=256)
@@ -267,6 +305,8 @@ def main(argv=None):
         out = tree_verify_bench(dev, ctx=args.ctx, iters=args.iters, n_layers=args.layers)
     elif args.case == "draft_forward":
         out = draft_forward_bench(dev, ctx=args.ctx, iters=args.iters)
+    elif args.case == "decode_stages":
+        out = decode_stage_table(dev, ctx=args.ctx if args.ctx != 256 else 520)
     elif args.case == "decode":
         out = decode_case(dev, args.prompt, args.gen, "nvfp4" if args.nvfp4 else "bf16")
     else:
