@@ -124,13 +124,13 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
                     Q35_TRY(gemm_bf16(a.normalized, HIDDEN, (const bf16*)L.p[slot[i]], rows[i], a.proj_buf + col, ldp, nullptr, 0, S, rows[i], HIDDEN, 0, 0, stream));
             }
             Q35_CUDA_OK(pdl_launch(pf_dn_prep_kernel, (S * DN_HEADS + DN_PREP_WARPS - 1) / DN_PREP_WARPS, 32 * DN_PREP_WARPS, 0, stream, a.proj_buf, ldp, (const bf16*)L.p[DN_CONV], (const bf16*)L.p[DN_ALOG],
-                                                                      (const bf16*)L.p[DN_DTBIAS], a.proj_buf2, a.beta_buf, a.alpha_buf, S));
-            Q35_CUDA_OK(pdl_launch(pf_conv_state_kernel, (DN_CONV_CH + 255) / 256, 256, 0, stream, a.proj_buf, ldp, a.conv_bufs + (size_t)i_dn * DN_CONV_CH * 4, S));
+                                                                      (const bf16*)L.p[DN_DTBIAS], a.proj_buf2, a.beta_buf, a.alpha_buf,
+                                                                      a.conv_bufs + (size_t)i_dn * DN_CONV_CH * 4, S));
             Q35_CUDA_OK(pdl_launch(pf_dn_chunk_local_kernel, dim3(nchunks, DN_HEADS), CL_THREADS, CHUNK_LOCAL_SMEM, stream, a.proj_buf2, a.beta_buf, a.alpha_buf, scratch, S, nchunks));
             Q35_CUDA_OK(pdl_launch(pf_dn_chunk_scan_kernel, dim3(DN_HEADS, DN_V / SCAN_VW), SCAN_THREADS, CHUNK_SCAN_SMEM, stream, 
                 scratch, a.dn_out_buf, a.dn_states + (size_t)i_dn * DN_HEADS * DN_V * DN_K, S, nchunks, err_word));
             Q35_CUDA_OK(pdl_launch(pf_gated_norm_kernel, (S * DN_HEADS + 7) / 8, 256, 0, stream, a.dn_out_buf, a.proj_buf, ldp, (const bf16*)L.p[DN_NORM], a.attn_buf, S));
-            g_launches.fetch_add(5);
+            g_launches.fetch_add(4);
             w_out = (const bf16*)L.p[DN_OUT]; w_post = (const bf16*)L.p[DN_POST_NORM]; w_down = (const bf16*)L.p[DN_DOWN];
             ++i_dn;
         } else {

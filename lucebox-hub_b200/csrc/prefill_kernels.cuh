@@ -120,11 +120,13 @@ static __global__ void __launch_bounds__(1024) pf_argmax_row_kernel(const bf16* 
 
 // ---- DeltaNet preparation: one warp per (token, head), a lane takes four adjacent dimensions of q, k and v ------------
 // proj: [S, ldp] bf16 rows [qkv 6144 | z 2048 | b 16 | a 16].  Writes qkv_out [S, 6144] bf16 (q, k L2-normalised
-// in bf16 arithmetic, v after conv + SiLU), beta [S,16] (bf16-rounded sigmoid), g [S,16] (f32 log-decay).
+// in bf16 arithmetic, v after conv + SiLU), beta [S,16] (bf16-rounded sigmoid), g [S,16] (f32 log-decay), and the conv window
+// the decode steps continue from.
 constexpr int DN_PREP_WARPS = 8;
 static __global__ void __launch_bounds__(32 * DN_PREP_WARPS) pf_dn_prep_kernel(const bf16* __restrict__ proj, int ldp, const bf16* __restrict__ conv_w,
                                                          const bf16* __restrict__ a_log, const bf16* __restrict__ dt_bias,
-                                                         bf16* __restrict__ qkv_out, float* __restrict__ beta, float* __restrict__ g, int S) {
+                                                         bf16* __restrict__ qkv_out, float* __restrict__ beta, float* __restrict__ g,
+                                                         float* __restrict__ conv_state, int S) {
     pdl_wait();
     const int unit = blockIdx.x * DN_PREP_WARPS + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (unit >= S * DN_HEADS) return;
@@ -141,6 +143,19 @@ static __global__ void __launch_bounds__(32 * DN_PREP_WARPS) pf_dn_prep_kernel(c
         for (int j = 0; j < 4; ++j) {
             const int tt = t - 3 + j;
             xr[j] = (tt >= 0) ? *reinterpret_cast<const uint2*>(proj + (size_t)tt * ldp + ch) : make_uint2(0u, 0u);
+        }
+        if (t == S - 1) {
+            // the last token's four taps are the conv window after the prompt: the last four inputs per channel, zero-padded
+            // on the left, newest last (f32 [channel][4])
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                float4 w;
+                w.x = (e & 1) ? bf_hi(e < 2 ? xr[0].x : xr[0].y) : bf_lo(e < 2 ? xr[0].x : xr[0].y);
+                w.y = (e & 1) ? bf_hi(e < 2 ? xr[1].x : xr[1].y) : bf_lo(e < 2 ? xr[1].x : xr[1].y);
+                w.z = (e & 1) ? bf_hi(e < 2 ? xr[2].x : xr[2].y) : bf_lo(e < 2 ? xr[2].x : xr[2].y);
+                w.w = (e & 1) ? bf_hi(e < 2 ? xr[3].x : xr[3].y) : bf_lo(e < 2 ? xr[3].x : xr[3].y);
+                reinterpret_cast<float4*>(conv_state)[ch + e] = w;
+            }
         }
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -181,21 +196,6 @@ static __global__ void __launch_bounds__(32 * DN_PREP_WARPS) pf_dn_prep_kernel(c
         const float sp = (x > 20.f) ? x : log1pf(expf(x));
         g[t * DN_HEADS + h] = -expf(bf2f(a_log[h])) * sp;
     }
-}
-
-// conv window after the prompt: the last four inputs per channel, zero-padded on the left, newest last
-static __global__ void pf_conv_state_kernel(const bf16* __restrict__ proj, int ldp, float* __restrict__ conv, int S) {
-    pdl_wait();
-    const int ch = blockIdx.x * blockDim.x + threadIdx.x;
-    if (ch >= DN_CONV_CH) return;
-    float4 st;
-    float* sv = reinterpret_cast<float*>(&st);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int tt = S - 4 + j;
-        sv[j] = (tt >= 0) ? bf2f(proj[(size_t)tt * ldp + ch]) : 0.f;
-    }
-    reinterpret_cast<float4*>(conv)[ch] = st;
 }
 
 // ---- TF32 tensor-core helpers (legacy mma.sync path, m16n8k8) --------------------------------------------------------
