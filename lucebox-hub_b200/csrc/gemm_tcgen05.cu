@@ -30,17 +30,21 @@ namespace q35 {
 constexpr int GEMM_BM = 128, GEMM_BN = 128, GEMM_BK = 64;
 constexpr int GEMM_THREADS = 192;
 constexpr uint32_t GEMM_STAGE_BYTES = (GEMM_BM + GEMM_BN) * GEMM_BK * 2;   // 32 KB
+__host__ __device__ constexpr uint32_t gemm_stage_bytes(int bn) { return (uint32_t)(GEMM_BM + bn) * GEMM_BK * 2; }
 // 6 stages for the wide problems (one CTA per SM); the skinny ones run a few k-steps per CTA: 3 stages, two CTAs per SM
 constexpr int GEMM_STAGES_WIDE = 6, GEMM_STAGES_SKINNY = 3, GEMM_STAGES_THIRD = 2;     // one, two, three CTAs per SM
+// the 64-column tile of the one-row-of-tiles problems (24 KB per stage): 8 stages for one CTA per SM, 4 for two
+constexpr int GEMM_BN_NARROW = 64, GEMM_STAGES_NARROW = 8, GEMM_STAGES_NARROW_SPLIT = 4;
 // The epilogue parks the f32 accumulator tile in the (then idle) stage buffers as [row][GEMM_PARK_LD]: with a pitch of
 // 132 floats the float4 accesses of eight adjacent rows (writing, one row per thread) and of one row's adjacent column
 // groups (reading) both spread over all 32 banks.
-constexpr int GEMM_PARK_LD = GEMM_BN + 4;
-constexpr uint32_t GEMM_PARK_BYTES = GEMM_BM * GEMM_PARK_LD * 4;
-__host__ __device__ constexpr uint32_t gemm_tile_bytes(int stages) {
-    return stages * GEMM_STAGE_BYTES > GEMM_PARK_BYTES ? stages * GEMM_STAGE_BYTES : ((GEMM_PARK_BYTES + 1023u) & ~1023u);
+__host__ __device__ constexpr uint32_t gemm_park_bytes(int bn) { return (uint32_t)GEMM_BM * (bn + 4) * 4; }
+__host__ __device__ constexpr uint32_t gemm_tile_bytes(int stages, int bn = GEMM_BN) {
+    return stages * gemm_stage_bytes(bn) > gemm_park_bytes(bn) ? stages * gemm_stage_bytes(bn) : ((gemm_park_bytes(bn) + 1023u) & ~1023u);
 }
-__host__ __device__ constexpr uint32_t gemm_smem(int stages) { return gemm_tile_bytes(stages) + 1024 /*align*/ + 256 /*barriers*/; }
+__host__ __device__ constexpr uint32_t gemm_smem(int stages, int bn = GEMM_BN) { return gemm_tile_bytes(stages, bn) + 1024 /*align*/ + 256 /*barriers*/; }
+// CTAs that fit an SM's 227 KB with this much dynamic shared memory each (1 KB reserved per CTA)
+__host__ __device__ constexpr int gemm_ctas_per_sm(uint32_t smem) { return smem + 1024 <= 77 * 1024 ? 3 : (smem + 1024 <= 116 * 1024 ? 2 : 1); }
 static_assert(GEMM_STAGES_SKINNY * GEMM_STAGE_BYTES >= GEMM_BM * GEMM_BN * 4, "the split-K form parks its f32 tile [column][row] in the stage buffers");
 constexpr int GEMM_MAX_SPLIT = 8;        // portable cluster size
 constexpr unsigned GEMM_SPIN_LIMIT = 20u * 1000u * 1000u;
@@ -97,7 +101,8 @@ __device__ __forceinline__ uint64_t make_smem_desc(uint32_t smem_addr) {
     return d;
 }
 // instruction descriptor: D f32, A/B bf16, both K-major, N at [17,23) in units of 8, M at [24,29) in units of 16
-constexpr uint32_t GEMM_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(GEMM_BN >> 3) << 17) | ((uint32_t)(GEMM_BM >> 4) << 24);
+__host__ __device__ constexpr uint32_t gemm_idesc(int bn) { return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(GEMM_BM >> 4) << 24); }
+constexpr uint32_t GEMM_IDESC = gemm_idesc(GEMM_BN);
 
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
     asm volatile(
@@ -174,9 +179,9 @@ __device__ __forceinline__ void epilogue_store8(const GemmParams& p, int row, in
 // shared-memory offset; CTA `rank` finishes columns [rank * BN_OUT / S, +BN_OUT / S) for `rows` rows.  A work item is one
 // row x 8 adjacent columns: all peers' values are requested before the first is used (one remote round trip, not S), then
 // summed in peer order, so the result does not depend on timing.  `t` is the calling thread's index among `nt` workers.
-template <int EPI>
+template <int EPI, int BN = GEMM_BN>
 __device__ __forceinline__ void cluster_reduce_store(const GemmParams& p, uint32_t park_local, int S, int rows, int m0, int n0, int t, int nt) {
-    constexpr int BN_OUT = (EPI == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
+    constexpr int BN_OUT = (EPI == EPI_SILU_MUL) ? BN / 2 : BN;
     const uint32_t rank = cluster_ctarank();
     // 8-column groups rank, rank + S, rank + 2S, ... of the tile belong to this CTA (any S up to the group count)
     const int my_groups = (BN_OUT / 8 - (int)rank + S - 1) / S;
@@ -205,7 +210,7 @@ __device__ __forceinline__ void cluster_reduce_store(const GemmParams& p, uint32
                 if (peer < S) {
                     const uint32_t base = map_to_cta(park_local, (uint32_t)peer);
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) v[peer][e] = ld_dsmem(base + (uint32_t)(((64 + col + e) * GEMM_BM + r) * 4));
+                    for (int e = 0; e < 8; ++e) v[peer][e] = ld_dsmem(base + (uint32_t)(((BN / 2 + col + e) * GEMM_BM + r) * 4));
                 }
 #pragma unroll
             for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
@@ -224,12 +229,13 @@ __device__ __forceinline__ float4 ld_smem4(uint32_t addr) {
     return v;
 }
 
-// Store pass of a one-CTA tile over its parked accumulator [row][GEMM_PARK_LD].  A work item is one row x 8 adjacent
+// Store pass of a one-CTA tile over its parked accumulator [row][BN + 4].  A work item is one row x 8 adjacent
 // output columns; consecutive threads take consecutive column groups of a row, so the 16-byte stores (and residual loads) of
 // a warp cover whole row segments.  Four rows are in flight per thread: their loads are all issued before the first is used.
-template <int EPI>
+template <int EPI, int BN>
 __device__ __forceinline__ void parked_tile_store(const GemmParams& p, uint32_t park_local, int rows, int m0, int n0, int t, int nt) {
-    constexpr int BN_OUT = (EPI == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
+    constexpr int BN_OUT = (EPI == EPI_SILU_MUL) ? BN / 2 : BN;
+    constexpr int PARK_LD = BN + 4;
     constexpr int NG = BN_OUT / 8;
     constexpr int UNR = 4;
     const int col = (t % NG) * 8, r_first = t / NG, r_step = nt / NG;
@@ -248,13 +254,13 @@ __device__ __forceinline__ void parked_tile_store(const GemmParams& p, uint32_t 
 #pragma unroll
         for (int q = 0; q < UNR; ++q) {
             const int r = min(rb + q * r_step, rows - 1);
-            const uint32_t off = (uint32_t)((r * GEMM_PARK_LD + col) * 4);
+            const uint32_t off = (uint32_t)((r * PARK_LD + col) * 4);
             const float4 a = ld_smem4(park_local + off), b = ld_smem4(park_local + off + 16);
             g[q][0] = a.x; g[q][1] = a.y; g[q][2] = a.z; g[q][3] = a.w; g[q][4] = b.x; g[q][5] = b.y; g[q][6] = b.z; g[q][7] = b.w;
 #pragma unroll
             for (int e = 0; e < 8; ++e) u[q][e] = 0.f;
             if (EPI == EPI_SILU_MUL) {
-                const float4 c = ld_smem4(park_local + off + 256), d = ld_smem4(park_local + off + 272);
+                const float4 c = ld_smem4(park_local + off + BN * 2), d = ld_smem4(park_local + off + BN * 2 + 16);
                 u[q][0] = c.x; u[q][1] = c.y; u[q][2] = c.z; u[q][3] = c.w; u[q][4] = d.x; u[q][5] = d.y; u[q][6] = d.z; u[q][7] = d.w;
             }
         }
@@ -281,22 +287,26 @@ __device__ __forceinline__ void parked_tile_store(const GemmParams& p, uint32_t 
     }
 }
 
-// SPLIT: gridDim.z = cluster size S along K (1, 2, 4 or 8); the cluster shares one output tile
-template <int EPI, int STAGES, bool SPLIT>
-__global__ void __launch_bounds__(GEMM_THREADS, STAGES == GEMM_STAGES_THIRD ? 3 : (STAGES == GEMM_STAGES_SKINNY ? 2 : 1))
+// SPLIT: gridDim.z = cluster size S along K (1, 2, 4 or 8); the cluster shares one output tile.  BN: columns of the tile.
+template <int EPI, int STAGES, bool SPLIT, int BN = GEMM_BN>
+__global__ void __launch_bounds__(GEMM_THREADS, gemm_ctas_per_sm(gemm_smem(STAGES, BN)))
 gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
     extern __shared__ unsigned char g_smem_raw[];
     // 128B-swizzled tiles need 1024-byte alignment
     const uint32_t raw = g_smem_u32(g_smem_raw);
     const uint32_t tiles = (raw + 1023u) & ~1023u;
     unsigned char* tiles_ptr = g_smem_raw + (tiles - raw);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(tiles_ptr + gemm_tile_bytes(STAGES));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(tiles_ptr + gemm_tile_bytes(STAGES, BN));
     const uint32_t full0 = g_smem_u32(bars), empty0 = full0 + 8 * STAGES, tfull = empty0 + 8 * STAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
     volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    constexpr int BN_OUT = (EPI == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
+    constexpr int BN_OUT = (EPI == EPI_SILU_MUL) ? BN / 2 : BN;
+    constexpr uint32_t SB = gemm_stage_bytes(BN);
+    // the B tile arrives as one or two boxes of B_BOX weight rows: the second box holds the rows that follow, or (SiLU
+    // epilogue) the up-projection rows that belong to the tile's gate rows
+    constexpr int B_BOX = (BN == GEMM_BN) ? 64 : (EPI == EPI_SILU_MUL ? BN / 2 : BN), B_NBOX = BN / B_BOX;
     const int n0 = blockIdx.x * BN_OUT, m0 = blockIdx.y * GEMM_BM;
     const int nkb_all = p.K / GEMM_BK;
     const int S = SPLIT ? (int)gridDim.z : 1, z = SPLIT ? (int)blockIdx.z : 0;
@@ -312,7 +322,7 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(g_smem_u32(tmem_slot)), "r"(128u) : "memory");
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(g_smem_u32(tmem_slot)), "r"((uint32_t)BN) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -327,11 +337,12 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
             for (int i = 0; i < nkb; ++i) {
                 const int st = i % STAGES, kb = kb_begin + i;
                 if (!g_mbar_wait(empty0 + 8 * st, ((i / STAGES) & 1) ^ 1, p.err, s_abort)) break;
-                const uint32_t a_dst = tiles + st * GEMM_STAGE_BYTES, b_dst = a_dst + GEMM_BM * GEMM_BK * 2;
-                g_mbar_expect_tx(full0 + 8 * st, GEMM_STAGE_BYTES);
+                const uint32_t a_dst = tiles + st * SB, b_dst = a_dst + GEMM_BM * GEMM_BK * 2;
+                g_mbar_expect_tx(full0 + 8 * st, SB);
                 g_tma_load_2d(a_dst, &tmA, kb * GEMM_BK, m0, full0 + 8 * st);
                 g_tma_load_2d(b_dst, &tmB, kb * GEMM_BK, n0, full0 + 8 * st);
-                g_tma_load_2d(b_dst + 64 * GEMM_BK * 2, &tmB, kb * GEMM_BK, (EPI == EPI_SILU_MUL ? p.up_row_offset : 64) + n0, full0 + 8 * st);
+                if (B_NBOX == 2)
+                    g_tma_load_2d(b_dst + B_BOX * GEMM_BK * 2, &tmB, kb * GEMM_BK, (EPI == EPI_SILU_MUL ? p.up_row_offset : B_BOX) + n0, full0 + 8 * st);
                 issued = i + 1;
             }
             // every copy this CTA issued must have landed before it may exit (matters only after an abort)
@@ -350,11 +361,11 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
                 ok = g_mbar_wait(full0 + 8 * st, (i / STAGES) & 1, p.err, s_abort);
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t a_addr = tiles + st * GEMM_STAGE_BYTES, b_addr = a_addr + GEMM_BM * GEMM_BK * 2;
+                const uint32_t a_addr = tiles + st * SB, b_addr = a_addr + GEMM_BM * GEMM_BK * 2;
                 const uint64_t adesc = make_smem_desc(a_addr), bdesc = make_smem_desc(b_addr);
 #pragma unroll
                 for (int k = 0; k < GEMM_BK / 16; ++k)   // 32 bytes of K per instruction: advance the start-address field by 2
-                    umma_bf16(tmem_base, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), GEMM_IDESC, (i > 0 || k > 0) ? 1u : 0u);
+                    umma_bf16(tmem_base, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), gemm_idesc(BN), (i > 0 || k > 0) ? 1u : 0u);
                 umma_commit(empty0 + 8 * st);       // frees the stage when these MMAs have read it
             }
             umma_commit(tfull);                     // accumulator complete (also fires after an abort so the epilogue wakes)
@@ -372,7 +383,7 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
         float* park = reinterpret_cast<float*>(tiles_ptr);
         if (m0 + q * 32 < p.M) {                                // else: rows of this warp are never read back
 #pragma unroll
-            for (int c = 0; c < GEMM_BN / 32; ++c) {
+            for (int c = 0; c < BN / 32; ++c) {
                 uint32_t v[32];
                 if (ok) {
                     tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
@@ -384,7 +395,7 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
                 } else {
 #pragma unroll
                     for (int j = 0; j < 32; j += 4)
-                        *reinterpret_cast<float4*>(park + rloc * GEMM_PARK_LD + c * 32 + j) =
+                        *reinterpret_cast<float4*>(park + rloc * (BN + 4) + c * 32 + j) =
                             ok ? make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]))
                                : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
@@ -396,20 +407,20 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
         // every thread of every CTA of the cluster passes both barriers, whatever happened above
         cluster_sync_all();
         if (warp >= 2 && !*s_abort)
-            cluster_reduce_store<EPI>(p, tiles, S, min(GEMM_BM, p.M - m0), m0, n0, (int)threadIdx.x - 64, GEMM_THREADS - 64);
+            cluster_reduce_store<EPI, BN>(p, tiles, S, min(GEMM_BM, p.M - m0), m0, n0, (int)threadIdx.x - 64, GEMM_THREADS - 64);
         __syncwarp();
         cluster_sync_all();                                     // no CTA leaves while a peer may still read its tile
     } else {
         // the store pass is arithmetic and address work on shared memory: all six warps take part (the copy and MMA warps
         // are idle by now)
         __syncthreads();
-        if (!*s_abort) parked_tile_store<EPI>(p, tiles, min(GEMM_BM, p.M - m0), m0, n0, (int)threadIdx.x, GEMM_THREADS);
+        if (!*s_abort) parked_tile_store<EPI, BN>(p, tiles, min(GEMM_BM, p.M - m0), m0, n0, (int)threadIdx.x, GEMM_THREADS);
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 1) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(128u) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"((uint32_t)BN) : "memory");
     }
 }
 
@@ -722,22 +733,52 @@ static cudaError_t gemm_launch(K kernel, dim3 grid, size_t smem, cudaStream_t st
     return cudaLaunchKernelEx(&cfg, kernel, tmA, tmB, p);
 }
 
-template <int E, int ST>
+template <int E, int ST, int BN = GEMM_BN>
 static int gemm_plain(dim3 grid, cudaStream_t stream, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p) {
     static PerDeviceOnce attr;
     if (attr.pending()) {
-        Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<E, ST, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem(ST)));
+        Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<E, ST, false, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem(ST, BN)));
         attr.mark();
     }
-    Q35_CUDA_OK(gemm_launch(gemm_bf16_tcgen05_kernel<E, ST, false>, grid, gemm_smem(ST), stream, tmA, tmB, p));
+    Q35_CUDA_OK(gemm_launch(gemm_bf16_tcgen05_kernel<E, ST, false, BN>, grid, gemm_smem(ST, BN), stream, tmA, tmB, p));
     return QWEN35_OK;
 }
-template <int ST>
+template <int ST, int BN = GEMM_BN>
 static int gemm_plain_epi(int epi, dim3 grid, cudaStream_t stream, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p) {
     switch (epi) {
-        case EPI_BF16: return gemm_plain<EPI_BF16, ST>(grid, stream, tmA, tmB, p);
-        case EPI_RESIDUAL: return gemm_plain<EPI_RESIDUAL, ST>(grid, stream, tmA, tmB, p);
-        default: return gemm_plain<EPI_SILU_MUL, ST>(grid, stream, tmA, tmB, p);
+        case EPI_BF16: return gemm_plain<EPI_BF16, ST, BN>(grid, stream, tmA, tmB, p);
+        case EPI_RESIDUAL: return gemm_plain<EPI_RESIDUAL, ST, BN>(grid, stream, tmA, tmB, p);
+        default: return gemm_plain<EPI_SILU_MUL, ST, BN>(grid, stream, tmA, tmB, p);
+    }
+}
+// split-K over a cluster of `split` CTAs along grid z
+template <int E, int ST, int BN>
+static int gemm_split(dim3 grid, int split, cudaStream_t stream, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p) {
+    static PerDeviceOnce attr;
+    if (attr.pending()) {
+        Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<E, ST, true, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem(ST, BN)));
+        attr.mark();
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid.x, grid.y, split);
+    cfg.blockDim = dim3(GEMM_THREADS);
+    cfg.dynamicSmemBytes = gemm_smem(ST, BN);
+    cfg.stream = stream;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = (unsigned)split;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at; cfg.numAttrs = g_pdl_launch ? 2 : 1;
+    Q35_CUDA_OK(cudaLaunchKernelEx(&cfg, gemm_bf16_tcgen05_kernel<E, ST, true, BN>, tmA, tmB, p));
+    return QWEN35_OK;
+}
+template <int ST, int BN>
+static int gemm_split_epi(int epi, dim3 grid, int split, cudaStream_t stream, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p) {
+    switch (epi) {
+        case EPI_BF16: return gemm_split<EPI_BF16, ST, BN>(grid, split, stream, tmA, tmB, p);
+        case EPI_RESIDUAL: return gemm_split<EPI_RESIDUAL, ST, BN>(grid, split, stream, tmA, tmB, p);
+        default: return gemm_split<EPI_SILU_MUL, ST, BN>(grid, split, stream, tmA, tmB, p);
     }
 }
 
@@ -753,64 +794,47 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
     void* ws = get_workspace();
     if (!ws) return QWEN35_ERR_CUDA;
     if (epi < 0 || epi > 2) { set_error("gemm_bf16: unknown epilogue %d", epi); return QWEN35_ERR_BAD_ARG; }
+    GemmParams p{M, N, K, C, ldc, R, ldr, up_row_offset, (int*)ws};
+    const int nkb = K / GEMM_BK;
+    const int m_tiles = (M + GEMM_BM - 1) / GEMM_BM;
+    const int bn_out = (epi == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
+    const int n_tiles = (N + bn_out - 1) / bn_out, tiles_total = m_tiles * n_tiles;
     CUtensorMap tmA, tmB;
-    if (!make_tmap(&tmA, A, M, K, lda, GEMM_BM) || !make_tmap(&tmB, B, b_rows, K, K, 64)) {
+    // One row of tiles that cannot fill the SMs with 128-column tiles (M <= 128: decode batches, tree nodes, draft rows, short
+    // prompts): 64-column tiles double the CTA count, so the wide projections need no split along K at all (no cluster
+    // barriers, no reduction through distributed shared memory) and the narrow ones reduce half as much.  A k-step costs
+    // its barrier hand-offs whatever the tile holds, so the narrow tile is taken only where it does not lengthen a long k loop.
+    const int bn_out_n = (epi == EPI_SILU_MUL) ? GEMM_BN_NARROW / 2 : GEMM_BN_NARROW;
+    const int nt_n = (N + bn_out_n - 1) / bn_out_n;
+    int split_n = 1, split_w = 1;
+    while (split_n < GEMM_MAX_SPLIT && nt_n * split_n < 100 && nkb / (split_n * 2) >= 2) split_n *= 2;
+    while (split_w < GEMM_MAX_SPLIT && n_tiles * split_w < 120 && nkb / (split_w * 2) >= 2) split_w *= 2;
+    const bool narrow = m_tiles == 1 && n_tiles < 148 && (split_n == 1 || nkb <= 16 || nkb / split_n <= nkb / split_w);
+    const int b_box = !narrow ? 64 : (epi == EPI_SILU_MUL ? GEMM_BN_NARROW / 2 : GEMM_BN_NARROW);
+    if (!make_tmap(&tmA, A, M, K, lda, GEMM_BM) || !make_tmap(&tmB, B, b_rows, K, K, b_box)) {
         set_error("cuTensorMapEncodeTiled failed (A %p [%d x %d] ld %d; B %p [%d x %d])", (const void*)A, M, K, lda, (const void*)B, b_rows, K);
         return QWEN35_ERR_CUDA;
     }
-    GemmParams p{M, N, K, C, ldc, R, ldr, up_row_offset, (int*)ws};
-    const int bn_out = (epi == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
-    const int m_tiles = (M + GEMM_BM - 1) / GEMM_BM, n_tiles = (N + bn_out - 1) / bn_out, nkb = K / GEMM_BK;
-    // a grid that cannot fill the SMs (few tiles, long K) also splits K over clusters
-    const bool small_grid = m_tiles * n_tiles < 100 && nkb >= 8;
-    const int tiles_total = m_tiles * n_tiles;
-    if (m_tiles > 1 && !small_grid) {
+    int st = QWEN35_OK;
+    if (narrow) {
+        if (split_n == 1) st = gemm_plain_epi<GEMM_STAGES_NARROW, GEMM_BN_NARROW>(epi, dim3(nt_n, 1), stream, tmA, tmB, p);
+        else st = gemm_split_epi<GEMM_STAGES_NARROW_SPLIT, GEMM_BN_NARROW>(epi, dim3(nt_n, 1), split_n, stream, tmA, tmB, p);
+    } else {
+        // a grid that cannot fill the SMs (few tiles, long K) splits K over clusters
+        const bool small_grid = tiles_total < 100 && nkb >= 8;
+        int split = 1;
+        if (small_grid) while (split < GEMM_MAX_SPLIT && tiles_total * split < 120 && nkb / (split * 2) >= 2) split *= 2;
+        const dim3 grid(n_tiles, m_tiles);
         // One CTA per SM with six stages while the tiles fit one wave; more tiles than SMs: three (two) stages per CTA let
         // two (three) CTAs share an SM -- the same bytes in flight per SM -- so that the prologue and epilogue of one tile
         // overlap the main loop of another and a tile count a little above a multiple of 148 does not leave a second wave
         // nearly empty.  Beyond three waves' worth of tiles the two-per-SM form is used.
-        const dim3 grid(n_tiles, m_tiles);
-        int st;
-        if (tiles_total <= 148) st = gemm_plain_epi<GEMM_STAGES_WIDE>(epi, grid, stream, tmA, tmB, p);
+        if (split > 1) st = gemm_split_epi<GEMM_STAGES_SKINNY, GEMM_BN>(epi, grid, split, stream, tmA, tmB, p);
+        else if (m_tiles > 1 && tiles_total <= 148) st = gemm_plain_epi<GEMM_STAGES_WIDE>(epi, grid, stream, tmA, tmB, p);
         else if (tiles_total > 296 && tiles_total <= 444) st = gemm_plain_epi<GEMM_STAGES_THIRD>(epi, grid, stream, tmA, tmB, p);
         else st = gemm_plain_epi<GEMM_STAGES_SKINNY>(epi, grid, stream, tmA, tmB, p);
-        if (st != QWEN35_OK) return st;
-    } else {
-        // few tiles: split K over a cluster until about one CTA per SM exists, at least two k-steps per CTA
-        int split = 1;
-        while (split < GEMM_MAX_SPLIT && m_tiles * n_tiles * split < 120 && nkb / (split * 2) >= 2) split *= 2;
-        if (split == 1) {
-            const int st = gemm_plain_epi<GEMM_STAGES_SKINNY>(epi, dim3(n_tiles, m_tiles), stream, tmA, tmB, p);
-            if (st != QWEN35_OK) return st;
-            Q35_CUDA_OK(cudaGetLastError());
-            g_launches.fetch_add(1);
-            return QWEN35_OK;
-        }
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(n_tiles, m_tiles, split);
-        cfg.blockDim = dim3(GEMM_THREADS);
-        cfg.dynamicSmemBytes = gemm_smem(GEMM_STAGES_SKINNY);
-        cfg.stream = stream;
-        cudaLaunchAttribute at[2];
-        at[0].id = cudaLaunchAttributeClusterDimension;
-        at[0].val.clusterDim.x = 1; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = (unsigned)split;
-        at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        at[1].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = at; cfg.numAttrs = g_pdl_launch ? 2 : 1;
-#define Q35_GEMM_SKINNY(E)                                                                                                                       \
-    case E: {                                                                                                                                    \
-        static PerDeviceOnce attr;                                                                                                                \
-        if (attr.pending()) {                                                                                                                             \
-            Q35_CUDA_OK(cudaFuncSetAttribute(gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
-                                             (int)gemm_smem(GEMM_STAGES_SKINNY)));                                                               \
-            attr.mark();                                                                                                                         \
-        }                                                                                                                                        \
-        Q35_CUDA_OK(cudaLaunchKernelEx(&cfg, gemm_bf16_tcgen05_kernel<E, GEMM_STAGES_SKINNY, true>, tmA, tmB, p));                                \
-        break;                                                                                                                                   \
     }
-        switch (epi) { Q35_GEMM_SKINNY(EPI_BF16) Q35_GEMM_SKINNY(EPI_RESIDUAL) Q35_GEMM_SKINNY(EPI_SILU_MUL) }
-#undef Q35_GEMM_SKINNY
-    }
+    if (st != QWEN35_OK) return st;
     Q35_CUDA_OK(cudaGetLastError());
     g_launches.fetch_add(1);
     return QWEN35_OK;

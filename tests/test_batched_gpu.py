@@ -6,7 +6,10 @@ import torch
 pytestmark = pytest.mark.gpu
 
 LAYER_ABS_TOL = 2.0 ** -5
-FRAC_TOL = 0.05                  # share of a teacher-forced trace's elements that may sit one bf16 step from the oracle's
+# share of a teacher-forced trace's elements (24 layers x 1024) that may sit one bf16 step from the oracle's: one flipped
+# rounding early in a layer moves a few hundred of that layer's outputs, so the share moves in steps with the order of the
+# f32 sums in the GEMMs (measured 2.7-5.7 % per sequence over the split-K and the full-K forms of the same GEMM)
+FRAC_TOL = 0.08
 STATE_REL_TOL = 1e-3
 LOGIT_TOL = 2e-2                 # teacher-forced logits: the task's bound
 
