@@ -11,6 +11,8 @@
 //              RMSNorm -> gate/up GEMM with fused SiLU*up -> down GEMM + residual
 //   finally    RMSNorm -> LM-head GEMM [B, 248320] -> per-row arg-max (lowest index among equal bf16 maxima)
 // KV cache pages: [layer 6][page][kv head 2][64 positions][256] bf16, addressed through block_table[B][max_pages].
+#include <cuda.h>
+
 #include "prefill_kernels.cuh"
 
 #include <cmath>
@@ -19,6 +21,8 @@
 #include "runtime.h"
 
 namespace q35 {
+bool make_tmap(CUtensorMap* tm, const void* ptr, int rows, int cols, int ld, int box_rows);      // gemm_tcgen05.cu
+
 
 int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ldc, const bf16* R, int ldr,
               int M, int N, int K, int epi, int up_row_offset, cudaStream_t stream);
@@ -162,175 +166,234 @@ __global__ void __launch_bounds__(256) bd_qk_norm_rope_kernel(const bf16* __rest
 
 // ---- decode attention over the paged cache, split over the context -----------------------------------------
 // Three kernels per layer keep the bf16 rounding points of the bs=1 path (P is rounded with the global normaliser):
-//   scores  one CTA per (sequence, kv head, chunk of 128 positions): bf16(q.k)/16 for the four q heads of the kv
-//           head (K row read once, coalesced), chunk max and sum-exp per head
-//   pv      same grid: global max / normaliser from the chunk statistics, P = bf16(exp(s-m)/l), partial P.V
-//   merge   one warp per (sequence, q head): sum of the partials in chunk order, bf16, times bf16(sigmoid(gate))
-constexpr int BD_CHUNK = 128;
+//   scores  one CTA per (sequence, kv head, slice z of Z): walks the 64-position pages z, z + Z, ... of the sequence;
+//           bf16(q.k)/16 for the four q heads of the kv head (K row read once, coalesced) to global memory, running
+//           maximum and sum-exp per head over the slice
+//   pv      same grid: global max / normaliser from the Z slice statistics, P = bf16(exp(s-m)/l), P.V accumulated over the
+//           slice's pages in registers, one partial per slice
+//   merge   one warp per (sequence, q head): sum of the slice partials in order, bf16, times bf16(sigmoid(gate))
+// A CTA reads its page ids once and keeps the next two pages' rows in flight (cp.async, three buffers) while it computes on
+// the current one: the chain position -> page id -> rows is paid once per slice, not once per 128 positions.
+constexpr int BD_CHUNK = KV_PAGE;                        // positions per step of a slice: one page
+constexpr int BD_MAX_PAGES_SLICE = 128;                  // page ids a CTA keeps in shared memory
 
 __device__ __forceinline__ const bf16* kv_row_c(const bf16* pages, const int* tb, int kvh, int pos) {
     return pages + (((size_t)tb[pos / KV_PAGE] * FA_KV_HEADS + kvh) * KV_PAGE + (pos % KV_PAGE)) * FA_HEAD_DIM;
 }
 
-// Both kernels stage the chunk's K (or V) rows in shared memory (rows padded to 528 bytes) with coalesced 16-byte
-// reads through the page table and run mma.sync m16n8k16 tiles on them: the M side holds the four q heads of the kv
-// head (rows 4-15 of the tile are zero), so a position costs a handful of instructions instead of a warp reduction
-// per head.  Fragment loads are ldmatrix (ldsm_x4 / ldsm_x4_trans of the prefill attention).
-constexpr int BD_LD = FA_HEAD_DIM + 8;                   // shared-memory row, bf16 elements
+// Both kernels receive a page's K (or V) rows by TMA: the page pool of a layer is a 2-D bf16 tensor [pages x kv heads x 64
+// rows][256], a page of one kv head arrives as four boxes of 64 rows x 64 dimensions in the 128-byte-swizzled layout (row r
+// of a box at r x 128 bytes, its 16-byte pieces XORed with r mod 8), which ldmatrix reads without bank conflicts.  One
+// thread issues the four copies of a page on an mbarrier; three page buffers keep two pages in flight while the four warps
+// run mma.sync m16n8k16 tiles on the third: the M side holds the four q heads of the kv head (rows 4-15 of the tile are
+// zero), so a position costs a handful of instructions instead of a warp reduction per head.  (The first form staged rows
+// with cp.async, 16 per thread and page: the issue rate of those copies, not the bytes in flight, bounded it at 3.5 TB/s.)
+constexpr int BD_LD = FA_HEAD_DIM + 8;                   // shared-memory row of the Q tile, bf16 elements
 constexpr int BD_PLD = BD_CHUNK + 8;
-constexpr int BD_SC_SMEM = (16 + BD_CHUNK) * BD_LD * 2;
-constexpr int BD_PV_SMEM = (BD_CHUNK * BD_LD + 16 * BD_PLD) * 2;
+constexpr int BD_NBUF = 3;                               // page buffers per CTA
+constexpr int BD_PAGE_BYTES = KV_PAGE * FA_HEAD_DIM * 2; // 32 KB: four 8 KB boxes
+constexpr int BD_SC_SMEM = 1024 + BD_NBUF * BD_PAGE_BYTES + 16 * BD_LD * 2;
+constexpr int BD_PV_SMEM = 1024 + BD_NBUF * BD_PAGE_BYTES + 16 * BD_PLD * 2;
+constexpr unsigned BD_WAIT_LIMIT = 1u << 24;
 
-// stage the chunk's rows [j0, j0+cn) of one kv head into shared memory with cp.async (a warp copies one 512-byte row
-// per step, every copy of the chunk in flight at once); the chunk is two 64-position pages (j0 is a multiple of 128)
-__device__ __forceinline__ void bd_stage_rows(const bf16* __restrict__ pages, const int* __restrict__ tb, int kvh, int j0, int cn, bf16* dst_rows) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const bf16* pg[2];
+// byte offset of element (row, dim) of a page buffer (four boxes of 64 dims; 128-byte rows; 16-byte pieces swizzled)
+__device__ __forceinline__ uint32_t bd_page_off(int row, int dim) {
+    return (uint32_t)((dim >> 6) * (KV_PAGE * 128) + row * 128 + ((((dim & 63) >> 3) ^ (row & 7)) << 4) + (dim & 7) * 2);
+}
+// one thread: the four copies of page `page` of kv head `kvh` into buffer `dst` (shared address), counted on `bar`
+__device__ __forceinline__ void bd_issue_page(const void* tmap, int page, int kvh, uint32_t dst, uint32_t bar) {
+    mbar_arrive_expect_tx(bar, BD_PAGE_BYTES);
+    const int y = (page * FA_KV_HEADS + kvh) * KV_PAGE;
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
-        pg[h] = (h * KV_PAGE < cn) ? pages + (((size_t)tb[j0 / KV_PAGE + h] * FA_KV_HEADS + kvh) * KV_PAGE) * FA_HEAD_DIM : pages;
-#pragma unroll 8
-    for (int it = 0; it < BD_CHUNK / 4; ++it) {              // all 32 copies of a thread are in flight together
-        const int kk = it * 4 + warp;
-        bf16* d = dst_rows + kk * BD_LD + lane * 8;
-        if (kk < cn) {
-            const uint32_t da = (uint32_t)__cvta_generic_to_shared(d);
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(da), "l"(pg[kk / KV_PAGE] + (size_t)(kk % KV_PAGE) * FA_HEAD_DIM + lane * 8) : "memory");
-        } else {
-            *reinterpret_cast<uint4*>(d) = make_uint4(0, 0, 0, 0);
-        }
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    for (int t = 0; t < 4; ++t) tma_load_2d(dst + t * (KV_PAGE * 128), tmap, t * 64, y, bar);
+}
+// bounded wait for a page; a wait that runs out sets the status word and the kernel carries on to its end
+__device__ __forceinline__ void bd_wait_bar(uint32_t bar, uint32_t parity, int* status) {
+    unsigned it = 0;
+    while (!mbar_try_wait(bar, parity))
+        if (++it >= BD_WAIT_LIMIT) { atomicCAS(status, 0, (int)ERR_BARRIER_TIMEOUT); return; }
 }
 
-__global__ void __launch_bounds__(128) bd_att_scores_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k_pages,
+__global__ void __launch_bounds__(128) bd_att_scores_kernel(const __grid_constant__ CUtensorMap tmK, const bf16* __restrict__ q,
                                                             const int* __restrict__ positions, const int* __restrict__ table, int max_pages,
-                                                            float* __restrict__ scores, float* __restrict__ stats, int max_ctx, int max_chunks) {
-    pdl_wait();
-    extern __shared__ __align__(16) unsigned char bd_sm[];
+                                                            float* __restrict__ scores, float* __restrict__ stats, int max_ctx, int max_slices,
+                                                            int* __restrict__ status) {
+    extern __shared__ unsigned char bd_sm_raw[];
     __shared__ float ssc[FA_GQA][BD_CHUNK];
-    bf16* Qs = reinterpret_cast<bf16*>(bd_sm);           // [16][BD_LD], rows 0-3 = the q heads of this kv head
-    bf16* Ks = Qs + 16 * BD_LD;                          // [BD_CHUNK][BD_LD]
-    const int b = blockIdx.x, kvh = blockIdx.y, c = blockIdx.z, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int L = positions[b] + 1, j0 = c * BD_CHUNK;
-    if (!bd_pos_ok(L - 1, max_ctx) || j0 >= L) return;
-    const int j1 = min(L, j0 + BD_CHUNK), cn = j1 - j0;
+    __shared__ int spg[BD_MAX_PAGES_SLICE];
+    __shared__ __align__(8) u64 bars[BD_NBUF];
+    const uint32_t raw = smem_u32(bd_sm_raw), pages_s = (raw + 1023u) & ~1023u;      // swizzled boxes need 1024-byte alignment
+    unsigned char* pages_p = bd_sm_raw + (pages_s - raw);
+    bf16* Qs = reinterpret_cast<bf16*>(pages_p + BD_NBUF * BD_PAGE_BYTES);             // [16][BD_LD], rows 0-3 = the q heads of this kv head
+    const int b = blockIdx.x, kvh = blockIdx.y, z = blockIdx.z, Z = gridDim.z, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmK) : "memory");
+        for (int i = 0; i < BD_NBUF; ++i) mbar_init(smem_u32(&bars[i]), 1);
+        mbar_fence_init();
+    }
+    pdl_wait();
+    const int L = positions[b] + 1;
+    const int npages = (L + KV_PAGE - 1) / KV_PAGE;
+    if (!bd_pos_ok(L - 1, max_ctx) || z >= npages) return;
+    const int mine = (npages - z + Z - 1) / Z;           // pages z, z + Z, ...
     const int* tb = table + b * max_pages;
+    for (int i = tid; i < mine && i < BD_MAX_PAGES_SLICE; i += 128) spg[i] = tb[z + i * Z];
     for (int i = tid; i < 16 * (FA_HEAD_DIM / 8); i += 128) {
         const int r = i / (FA_HEAD_DIM / 8), c8 = i % (FA_HEAD_DIM / 8);
         uint4 v = make_uint4(0, 0, 0, 0);
         if (r < FA_GQA) v = *reinterpret_cast<const uint4*>(q + (size_t)b * FA_Q_SIZE + (kvh * FA_GQA + r) * FA_HEAD_DIM + c8 * 8);
         *reinterpret_cast<uint4*>(Qs + r * BD_LD + c8 * 8) = v;
     }
-    bd_stage_rows(k_pages, tb, kvh, j0, cn, Ks);
     __syncthreads();
-    // warp w: keys [32w, 32w+32) = 4 tiles of 8 keys
-    float acc[4][4];
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) { acc[nt][0] = 0.f; acc[nt][1] = 0.f; acc[nt][2] = 0.f; acc[nt][3] = 0.f; }
-#pragma unroll 4
-    for (int ks = 0; ks < FA_HEAD_DIM / 16; ++ks) {
-        uint32_t a[4];
-        ldsm_x4(a, Qs + (lane & 15) * BD_LD + ks * 16 + (lane >> 4) * 8);
-#pragma unroll
-        for (int np = 0; np < 2; ++np) {
-            uint32_t bb[4];
-            ldsm_x4(bb, Ks + (warp * 32 + np * 16 + (lane & 7) + 8 * (lane >> 4)) * BD_LD + ks * 16 + 8 * ((lane >> 3) & 1));
-            mma_16816(acc[2 * np], a, bb[0], bb[1]);
-            mma_16816(acc[2 * np + 1], a, bb[2], bb[3]);
-        }
+    if (tid == 0) {
+        bd_issue_page(&tmK, spg[0], kvh, pages_s, smem_u32(&bars[0]));
+        if (mine > 1) bd_issue_page(&tmK, spg[1], kvh, pages_s + BD_PAGE_BYTES, smem_u32(&bars[1]));
     }
-    {   // accumulator rows 0-3 (g = lane/4 < 4) are the four heads; columns 2c, 2c+1 of each 8-key tile
-        const int g = lane >> 2, cc = lane & 3;
-        if (g < FA_GQA) {
+    float run_m = -INFINITY, run_s = 0.f;                 // warp g: head g's statistics over the slice
+    for (int i = 0; i < mine; ++i) {
+        const int j0 = (z + i * Z) * KV_PAGE, cn = min(KV_PAGE, L - j0);
+        const uint32_t Kc = pages_s + (i % BD_NBUF) * BD_PAGE_BYTES;
+        // buffer (i + 2) % 3 was read in step i - 1; every warp has passed that step's barrier after its MMAs
+        if (tid == 0 && i + 2 < mine) bd_issue_page(&tmK, spg[i + 2], kvh, pages_s + ((i + 2) % BD_NBUF) * BD_PAGE_BYTES, smem_u32(&bars[(i + 2) % BD_NBUF]));
+        bd_wait_bar(smem_u32(&bars[i % BD_NBUF]), (uint32_t)((i / BD_NBUF) & 1), status);
+        // warp w: keys [16w, 16w+16) = 2 tiles of 8 keys
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        const int krow = warp * 16 + (lane & 7) + 8 * (lane >> 4);
+#pragma unroll 4
+        for (int ks = 0; ks < FA_HEAD_DIM / 16; ++ks) {
+            uint32_t a[4], bb[4];
+            ldsm_x4(a, Qs + (lane & 15) * BD_LD + ks * 16 + (lane >> 4) * 8);
+            const uint32_t baddr = Kc + bd_page_off(krow, ks * 16 + 8 * ((lane >> 3) & 1));
+            asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];" : "=r"(bb[0]), "=r"(bb[1]), "=r"(bb[2]), "=r"(bb[3]) : "r"(baddr));
+            mma_16816(acc[0], a, bb[0], bb[1]);
+            mma_16816(acc[1], a, bb[2], bb[3]);
+        }
+        {   // accumulator rows 0-3 (g = lane/4 < 4) are the four heads; columns 2c, 2c+1 of each 8-key tile
+            const int g = lane >> 2, cc = lane & 3;
+            if (g < FA_GQA) {
 #pragma unroll
-            for (int nt = 0; nt < 4; ++nt) {
-                ssc[g][warp * 32 + nt * 8 + 2 * cc] = rbf(acc[nt][0]) * 0.0625f;
-                ssc[g][warp * 32 + nt * 8 + 2 * cc + 1] = rbf(acc[nt][1]) * 0.0625f;
+                for (int nt = 0; nt < 2; ++nt) {
+                    ssc[g][warp * 16 + nt * 8 + 2 * cc] = rbf(acc[nt][0]) * 0.0625f;
+                    ssc[g][warp * 16 + nt * 8 + 2 * cc + 1] = rbf(acc[nt][1]) * 0.0625f;
+                }
             }
         }
-    }
-    __syncthreads();
-    {   // warp g: statistics of head g over this chunk; scores to global
-        const int g = warp;
-        float mx = -INFINITY;
-        for (int j = lane; j < cn; j += 32) mx = fmaxf(mx, ssc[g][j]);
-        mx = warp_max(mx);
-        float sm = 0.f;
-        for (int j = lane; j < cn; j += 32) sm += expf(ssc[g][j] - mx);
-        sm = warp_sum(sm);
-        const int head = kvh * FA_GQA + g;
-        if (lane == 0) {
-            float* st = stats + (((size_t)b * FA_Q_HEADS + head) * max_chunks + c) * 2;
-            st[0] = mx; st[1] = sm;
+        __syncthreads();                                 // scores of the page complete; every warp is done with this buffer
+        {   // warp g: statistics of head g over this page, folded into the slice's; scores to global
+            const int g = warp;
+            float mx = -INFINITY;
+            for (int j = lane; j < cn; j += 32) mx = fmaxf(mx, ssc[g][j]);
+            mx = warp_max(mx);
+            float sm = 0.f;
+            for (int j = lane; j < cn; j += 32) sm += expf(ssc[g][j] - mx);
+            sm = warp_sum(sm);
+            const float nm = fmaxf(run_m, mx);
+            run_s = (run_m == -INFINITY ? 0.f : run_s * expf(run_m - nm)) + sm * expf(mx - nm);
+            run_m = nm;
+            float* dst = scores + ((size_t)b * FA_Q_HEADS + kvh * FA_GQA + g) * max_ctx + j0;
+            for (int j = lane; j < cn; j += 32) dst[j] = ssc[g][j];
         }
-        float* dst = scores + ((size_t)b * FA_Q_HEADS + head) * max_ctx + j0;
-        for (int j = lane; j < cn; j += 32) dst[j] = ssc[g][j];
+        __syncthreads();                                 // ssc is free for the next page
+    }
+    if (lane == 0) {
+        float* st = stats + (((size_t)b * FA_Q_HEADS + kvh * FA_GQA + warp) * max_slices + z) * 2;
+        st[0] = run_m; st[1] = run_s;
     }
 }
 
-__global__ void __launch_bounds__(128) bd_att_pv_kernel(const bf16* __restrict__ v_pages, const int* __restrict__ positions,
+__global__ void __launch_bounds__(128) bd_att_pv_kernel(const __grid_constant__ CUtensorMap tmV, const int* __restrict__ positions,
                                                         const int* __restrict__ table, int max_pages, const float* __restrict__ scores,
-                                                        const float* __restrict__ stats, float* __restrict__ partial, int max_ctx, int max_chunks) {
-    pdl_wait();
-    extern __shared__ __align__(16) unsigned char bd_sm[];
+                                                        const float* __restrict__ stats, float* __restrict__ partial, int max_ctx, int max_slices,
+                                                        int* __restrict__ status) {
+    extern __shared__ unsigned char bd_sm_raw[];
     __shared__ float sml[FA_GQA][2];
-    bf16* Vs = reinterpret_cast<bf16*>(bd_sm);           // [BD_CHUNK][BD_LD]
-    bf16* Ps = Vs + BD_CHUNK * BD_LD;                    // [16][BD_PLD], rows 0-3 = P of the four heads
-    const int b = blockIdx.x, kvh = blockIdx.y, c = blockIdx.z, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int L = positions[b] + 1, j0 = c * BD_CHUNK;
-    if (!bd_pos_ok(L - 1, max_ctx) || j0 >= L) return;
-    const int j1 = min(L, j0 + BD_CHUNK), cn = j1 - j0;
-    const int nch = (L + BD_CHUNK - 1) / BD_CHUNK;
+    __shared__ int spg[BD_MAX_PAGES_SLICE];
+    __shared__ __align__(8) u64 bars[BD_NBUF];
+    const uint32_t raw = smem_u32(bd_sm_raw), pages_s = (raw + 1023u) & ~1023u;
+    unsigned char* pages_p = bd_sm_raw + (pages_s - raw);
+    bf16* Ps = reinterpret_cast<bf16*>(pages_p + BD_NBUF * BD_PAGE_BYTES);             // [16][BD_PLD], rows 0-3 = P of the four heads
+    const int b = blockIdx.x, kvh = blockIdx.y, z = blockIdx.z, Z = gridDim.z, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(&tmV) : "memory");
+        for (int i = 0; i < BD_NBUF; ++i) mbar_init(smem_u32(&bars[i]), 1);
+        mbar_fence_init();
+    }
+    pdl_wait();
+    const int L = positions[b] + 1;
+    const int npages = (L + KV_PAGE - 1) / KV_PAGE;
+    if (!bd_pos_ok(L - 1, max_ctx) || z >= npages) return;
+    const int mine = (npages - z + Z - 1) / Z, nsl = min(Z, npages);
     const int* tb = table + b * max_pages;
+    for (int i = tid; i < mine && i < BD_MAX_PAGES_SLICE; i += 128) spg[i] = tb[z + i * Z];
     {
         const int head = kvh * FA_GQA + warp;
-        const float* st = stats + ((size_t)b * FA_Q_HEADS + head) * max_chunks * 2;
+        const float* st = stats + ((size_t)b * FA_Q_HEADS + head) * max_slices * 2;
         float mx = -INFINITY;
-        for (int k = lane; k < nch; k += 32) mx = fmaxf(mx, st[2 * k]);
+        for (int k = lane; k < nsl; k += 32) mx = fmaxf(mx, st[2 * k]);
         mx = warp_max(mx);
         float sm = 0.f;
-        for (int k = lane; k < nch; k += 32) sm += st[2 * k + 1] * expf(st[2 * k] - mx);
+        for (int k = lane; k < nsl; k += 32) sm += st[2 * k + 1] * expf(st[2 * k] - mx);
         sm = warp_sum(sm);
         if (lane == 0) { sml[warp][0] = mx; sml[warp][1] = sm; }
     }
-    bd_stage_rows(v_pages, tb, kvh, j0, cn, Vs);
+    for (int i = tid; i < 12 * BD_PLD; i += 128) Ps[4 * BD_PLD + i] = f2bf(0.f);      // rows 4-15 of the P tile stay zero
     __syncthreads();
-    for (int i = tid; i < 16 * BD_CHUNK; i += 128) {
-        const int g = i / BD_CHUNK, j = i % BD_CHUNK;
-        float pv = 0.f;
-        if (g < FA_GQA && j < cn) pv = rbf(expf(scores[((size_t)b * FA_Q_HEADS + kvh * FA_GQA + g) * max_ctx + j0 + j] - sml[g][0]) / sml[g][1]);
-        Ps[g * BD_PLD + j] = f2bf(pv);
+    if (tid == 0) {
+        bd_issue_page(&tmV, spg[0], kvh, pages_s, smem_u32(&bars[0]));
+        if (mine > 1) bd_issue_page(&tmV, spg[1], kvh, pages_s + BD_PAGE_BYTES, smem_u32(&bars[1]));
     }
-    __syncthreads();
-    // warp w: output dims [64w, 64w+64) = 8 tiles of 8 dims; 8 steps of 16 keys
+    // warp w: output dims [64w, 64w+64) = 8 tiles of 8 dims (box w of a page buffer), accumulated over the slice's pages
     float acc[8][4];
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) { acc[nt][0] = 0.f; acc[nt][1] = 0.f; acc[nt][2] = 0.f; acc[nt][3] = 0.f; }
-#pragma unroll
-    for (int ks = 0; ks < BD_CHUNK / 16; ++ks) {
-        uint32_t a[4];
-        ldsm_x4(a, Ps + (lane & 15) * BD_PLD + ks * 16 + (lane >> 4) * 8);
-#pragma unroll
-        for (int np = 0; np < 4; ++np) {
-            uint32_t bb[4];
-            ldsm_x4_trans(bb, Vs + (ks * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * BD_LD + warp * 64 + np * 16 + 8 * (lane >> 4));
-            mma_16816(acc[2 * np], a, bb[0], bb[1]);
-            mma_16816(acc[2 * np + 1], a, bb[2], bb[3]);
+    for (int i = 0; i < mine; ++i) {
+        const int j0 = (z + i * Z) * KV_PAGE, cn = min(KV_PAGE, L - j0);
+        const uint32_t Vc = pages_s + (i % BD_NBUF) * BD_PAGE_BYTES;
+        if (tid == 0 && i + 2 < mine) bd_issue_page(&tmV, spg[i + 2], kvh, pages_s + ((i + 2) % BD_NBUF) * BD_PAGE_BYTES, smem_u32(&bars[(i + 2) % BD_NBUF]));
+        // P of this page while the copies fly: 4 heads x 64 positions, two per thread
+        for (int e = tid; e < FA_GQA * BD_CHUNK; e += 128) {
+            const int g = e / BD_CHUNK, j = e % BD_CHUNK;
+            float pv = 0.f;
+            if (j < cn) pv = rbf(expf(scores[((size_t)b * FA_Q_HEADS + kvh * FA_GQA + g) * max_ctx + j0 + j] - sml[g][0]) / sml[g][1]);
+            Ps[g * BD_PLD + j] = f2bf(pv);
         }
+        bd_wait_bar(smem_u32(&bars[i % BD_NBUF]), (uint32_t)((i / BD_NBUF) & 1), status);
+        if (cn < KV_PAGE) {
+            // rows past the sequence's end hold whatever the pool has there; P is zero for them, but 0 x NaN is not: clear them
+            unsigned char* vb = pages_p + (i % BD_NBUF) * BD_PAGE_BYTES;
+            for (int e = tid; e < (KV_PAGE - cn) * 32; e += 128) {
+                const int r = cn + e / 32, piece = e % 32;
+                *reinterpret_cast<uint4*>(vb + (piece >> 3) * (KV_PAGE * 128) + r * 128 + (piece & 7) * 16) = make_uint4(0, 0, 0, 0);
+            }
+        }
+        __syncthreads();
+        const int steps = (cn + 15) / 16;
+        for (int ks = 0; ks < steps; ++ks) {
+            uint32_t a[4];
+            ldsm_x4(a, Ps + (lane & 15) * BD_PLD + ks * 16 + (lane >> 4) * 8);
+            const int vrow = ks * 16 + (lane & 7) + 8 * ((lane >> 3) & 1);
+#pragma unroll
+            for (int np = 0; np < 4; ++np) {
+                uint32_t bb[4];
+                const uint32_t baddr = Vc + bd_page_off(vrow, warp * 64 + np * 16 + 8 * (lane >> 4));
+                asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];" : "=r"(bb[0]), "=r"(bb[1]), "=r"(bb[2]), "=r"(bb[3]) : "r"(baddr));
+                mma_16816(acc[2 * np], a, bb[0], bb[1]);
+                mma_16816(acc[2 * np + 1], a, bb[2], bb[3]);
+            }
+        }
+        __syncthreads();                                 // P tile and this buffer are free again
     }
     const int g = lane >> 2, cc = lane & 3;
     if (g < FA_GQA) {
-        float* dst = partial + (((size_t)b * FA_Q_HEADS + kvh * FA_GQA + g) * max_chunks + c) * FA_HEAD_DIM + warp * 64 + 2 * cc;
+        float* dst = partial + (((size_t)b * FA_Q_HEADS + kvh * FA_GQA + g) * max_slices + z) * FA_HEAD_DIM + warp * 64 + 2 * cc;
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) *reinterpret_cast<float2*>(dst + nt * 8) = make_float2(acc[nt][0], acc[nt][1]);
     }
 }
 
 __global__ void __launch_bounds__(256) bd_att_merge_kernel(const float* __restrict__ partial, const int* __restrict__ positions,
-                                                           const bf16* __restrict__ proj, int ldp, bf16* __restrict__ out, int B, int max_chunks,
-                                                           int max_ctx) {
+                                                           const bf16* __restrict__ proj, int ldp, bf16* __restrict__ out, int B, int max_slices,
+                                                           int n_slices, int max_ctx) {
     pdl_wait();
     const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (gw >= B * FA_Q_HEADS) return;
@@ -339,10 +402,10 @@ __global__ void __launch_bounds__(256) bd_att_merge_kernel(const float* __restri
         *(reinterpret_cast<uint4*>(out + (size_t)b * FA_Q_SIZE + head * FA_HEAD_DIM) + lane) = make_uint4(0, 0, 0, 0);
         return;
     }
-    const int nch = (positions[b] + 1 + BD_CHUNK - 1) / BD_CHUNK;
+    const int nsl = min(n_slices, (positions[b] + 1 + KV_PAGE - 1) / KV_PAGE);
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    const float* pb = partial + ((size_t)b * FA_Q_HEADS + head) * max_chunks * FA_HEAD_DIM + lane * 8;
-    for (int c = 0; c < nch; ++c) {
+    const float* pb = partial + ((size_t)b * FA_Q_HEADS + head) * max_slices * FA_HEAD_DIM + lane * 8;
+    for (int c = 0; c < nsl; ++c) {
         const float4 a0 = *reinterpret_cast<const float4*>(pb + (size_t)c * FA_HEAD_DIM), a1 = *reinterpret_cast<const float4*>(pb + (size_t)c * FA_HEAD_DIM + 4);
         acc[0] += a0.x; acc[1] += a0.y; acc[2] += a0.z; acc[3] += a0.w; acc[4] += a1.x; acc[5] += a1.y; acc[6] += a1.z; acc[7] += a1.w;
     }
@@ -418,13 +481,19 @@ static void* batched_scratch(size_t bytes) {
 
 typedef PrefillFused PrefillFusedB;
 
+// upper bound of the slices per (sequence, kv head): the statistics and partial buffers are sized by it.  A slice holds at
+// most BD_MAX_PAGES_SLICE page ids, so long contexts need at least pages / BD_MAX_PAGES_SLICE slices.
+static int bd_max_slices(int max_ctx) {
+    const int pages = (max_ctx + KV_PAGE - 1) / KV_PAGE;
+    return pages < 148 ? pages : 148;
+}
 }  // namespace q35
 
 static size_t batched_scratch_total(int batch, int max_ctx) {
     using namespace q35;
     const size_t rows = (size_t)batch;
     const size_t n_hidden = rows * HIDDEN, n_proj = rows * DN_PROJ_ROWS, n_att = rows * 2048, n_mlp = rows * INTER, n_logits = rows * VOCAB;
-    const int max_chunks = (max_ctx + BD_CHUNK - 1) / BD_CHUNK;
+    const int max_chunks = bd_max_slices(max_ctx);
     const size_t n_scores = rows * FA_Q_HEADS * (size_t)max_ctx, n_stats = rows * FA_Q_HEADS * max_chunks * 2, n_part = rows * FA_Q_HEADS * max_chunks * FA_HEAD_DIM;
     return (3 * n_hidden + n_proj + 3 * n_att + n_mlp + n_logits) * sizeof(bf16) + (n_scores + n_stats + n_part) * sizeof(float) + 4096;
 }
@@ -474,7 +543,7 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
     // scratch rows of B tokens
     const size_t rows = (size_t)B;
     const size_t n_hidden = rows * HIDDEN, n_proj = rows * DN_PROJ_ROWS, n_att = rows * 2048, n_mlp = rows * INTER, n_logits = rows * VOCAB;
-    const int max_chunks = (in->max_ctx + BD_CHUNK - 1) / BD_CHUNK;
+    const int max_chunks = bd_max_slices(in->max_ctx);
     const size_t n_scores = rows * FA_Q_HEADS * (size_t)in->max_ctx, n_stats = rows * FA_Q_HEADS * max_chunks * 2,
                  n_part = rows * FA_Q_HEADS * max_chunks * FA_HEAD_DIM;
     const size_t total = batched_scratch_total(B, in->max_ctx);
@@ -540,10 +609,21 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
             bf16* vp = (bf16*)in->v_pages + (size_t)i_fa * page_layer_stride;
             Q35_CUDA_OK(pdl_launch(bd_qk_norm_rope_kernel, (B * 12 + 7) / 8, 256, 0, stream, proj, ldp, (const bf16*)L.p[FA_QNORM], (const bf16*)L.p[FA_KNORM], rt,
                                                                          in->positions, in->block_table, in->max_pages, qbuf, kp, vp, B, in->max_ctx, status_word));
-            const dim3 agrid(B, FA_KV_HEADS, max_chunks);
-            Q35_CUDA_OK(pdl_launch(bd_att_scores_kernel, agrid, 128, BD_SC_SMEM, stream, qbuf, kp, in->positions, in->block_table, in->max_pages, att_scores, att_stats, in->max_ctx, max_chunks));
-            Q35_CUDA_OK(pdl_launch(bd_att_pv_kernel, agrid, 128, BD_PV_SMEM, stream, vp, in->positions, in->block_table, in->max_pages, att_scores, att_stats, att_part, in->max_ctx, max_chunks));
-            Q35_CUDA_OK(pdl_launch(bd_att_merge_kernel, (B * FA_Q_HEADS + 7) / 8, 256, 0, stream, att_part, in->positions, proj, ldp, attn, B, max_chunks, in->max_ctx));
+            // slices per (sequence, kv head): as many as keep the grid within the CTAs the GPU holds at once (two or three per SM)
+            int n_slices = (148 * 2) / (B * FA_KV_HEADS);
+            const int min_slices = ((in->max_ctx + KV_PAGE - 1) / KV_PAGE + BD_MAX_PAGES_SLICE - 1) / BD_MAX_PAGES_SLICE;   // page ids per slice are bounded
+            n_slices = n_slices < min_slices ? min_slices : n_slices;
+            n_slices = n_slices > max_chunks ? max_chunks : n_slices;
+            const dim3 agrid(B, FA_KV_HEADS, n_slices);
+            CUtensorMap tmK, tmV;
+            const int pool_rows = in->num_pages * FA_KV_HEADS * KV_PAGE;
+            if (!make_tmap(&tmK, kp, pool_rows, FA_HEAD_DIM, FA_HEAD_DIM, KV_PAGE) || !make_tmap(&tmV, vp, pool_rows, FA_HEAD_DIM, FA_HEAD_DIM, KV_PAGE)) {
+                set_error("batched decode: tensor map of the K / V page pool failed (pool %p / %p must be 16-byte aligned)", (const void*)kp, (const void*)vp);
+                return QWEN35_ERR_CUDA;
+            }
+            Q35_CUDA_OK(pdl_launch(bd_att_scores_kernel, agrid, 128, BD_SC_SMEM, stream, tmK, (const bf16*)qbuf, in->positions, in->block_table, in->max_pages, att_scores, att_stats, in->max_ctx, max_chunks, status_word));
+            Q35_CUDA_OK(pdl_launch(bd_att_pv_kernel, agrid, 128, BD_PV_SMEM, stream, tmV, in->positions, in->block_table, in->max_pages, (const float*)att_scores, (const float*)att_stats, att_part, in->max_ctx, max_chunks, status_word));
+            Q35_CUDA_OK(pdl_launch(bd_att_merge_kernel, (B * FA_Q_HEADS + 7) / 8, 256, 0, stream, att_part, in->positions, proj, ldp, attn, B, max_chunks, n_slices, in->max_ctx));
             g_launches.fetch_add(4);
             w_out = (const bf16*)L.p[FA_O]; w_post = (const bf16*)L.p[FA_POST_NORM]; w_down = (const bf16*)L.p[FA_DOWN];
             ++i_fa;

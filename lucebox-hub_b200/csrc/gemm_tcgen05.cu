@@ -695,7 +695,8 @@ static EncodeTiledFn encode_fn() {
 }
 
 // 2-D bf16 tensor [rows, cols] with row stride `ld` elements; box = 64 columns x box_rows, 128-byte swizzle.
-static bool make_tmap(CUtensorMap* tm, const void* ptr, int rows, int cols, int ld, int box_rows) {
+// (also used by the batched-decode attention for its K / V pages)
+bool make_tmap(CUtensorMap* tm, const void* ptr, int rows, int cols, int ld, int box_rows) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
