@@ -777,9 +777,15 @@ constexpr int ATT_PF_MAX_S = 4096;      // longest prompt the prefill entry poin
 // key range: pass 1 the running row maximum and normaliser from bf16(q.k)/16; pass 2 recomputes the same scores (same
 // instructions, same values), forms P = bf16(exp(s - m) / l) in registers (the accumulator layout of two adjacent
 // 8-key tiles is the A-operand layout of a 16-key step) and accumulates P.V.  Fragments come from ldmatrix on rows
-// padded to 528 bytes (conflict-free); V is read with ldmatrix.trans.
+// padded to 528 bytes (conflict-free); V is read with ldmatrix.trans.  K (and V in pass 2) chunks arrive by cp.async into
+// two buffers: the next chunk's copies fly while this one is computed on, one __syncthreads per chunk.
 constexpr int ATT_MMA_Q = 32, ATT_MMA_ROWS = ATT_MMA_Q * FA_GQA, ATT_MMA_KEYS = 64, ATT_MMA_LD = FA_HEAD_DIM + 8;
-constexpr int ATT_MMA_SMEM = (ATT_MMA_ROWS + 2 * ATT_MMA_KEYS) * ATT_MMA_LD * 2;
+constexpr int ATT_MMA_SMEM = (ATT_MMA_ROWS + 4 * ATT_MMA_KEYS) * ATT_MMA_LD * 2;      // Q tile + two (K, V) chunk buffers
+
+__device__ __forceinline__ void att_cp16(bf16* dst, const bf16* src, bool valid) {
+    const int n = valid ? 16 : 0;        // 0 source bytes: the 16 destination bytes are zero-filled
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src), "r"(n) : "memory");
+}
 
 static __global__ void __launch_bounds__(256, 1) pf_attention_mma_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k_cache,
                                                                   const bf16* __restrict__ v_cache, const bf16* __restrict__ proj, int ldp,
@@ -787,21 +793,34 @@ static __global__ void __launch_bounds__(256, 1) pf_attention_mma_kernel(const b
     pdl_wait();
     extern __shared__ __align__(16) unsigned char att_mma_sm[];
     bf16* Qs = reinterpret_cast<bf16*>(att_mma_sm);
-    bf16* Ks = Qs + ATT_MMA_ROWS * ATT_MMA_LD;
-    bf16* Vs = Ks + ATT_MMA_KEYS * ATT_MMA_LD;
+    bf16* KV = Qs + ATT_MMA_ROWS * ATT_MMA_LD;                    // [buffer 2][K, V][64][LD]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
     const int blk = (int)gridDim.x - 1 - (int)blockIdx.x;          // long blocks first
     const int kvh = blockIdx.y, q0 = blk * ATT_MMA_Q;
     const bf16* kb = k_cache + (size_t)kvh * max_seq * FA_HEAD_DIM;
     const bf16* vb = v_cache + (size_t)kvh * max_seq * FA_HEAD_DIM;
+    const int t_last = min(q0 + ATT_MMA_Q, S) - 1;
+    const int nchunks = t_last / ATT_MMA_KEYS + 1, nitems = 2 * nchunks;
+    auto stage = [&](int item) {
+        const int pass = item >= nchunks, j0 = (pass ? item - nchunks : item) * ATT_MMA_KEYS;
+        bf16* kd = KV + (size_t)(item & 1) * 2 * ATT_MMA_KEYS * ATT_MMA_LD;
+        bf16* vd = kd + ATT_MMA_KEYS * ATT_MMA_LD;
+        for (int i = tid; i < ATT_MMA_KEYS * (FA_HEAD_DIM / 8); i += 256) {
+            const int kk = i / (FA_HEAD_DIM / 8), c8 = i % (FA_HEAD_DIM / 8);
+            const bool ok = j0 + kk < S;
+            const size_t off = (size_t)(ok ? j0 + kk : 0) * FA_HEAD_DIM + c8 * 8;
+            att_cp16(kd + kk * ATT_MMA_LD + c8 * 8, kb + off, ok);
+            if (pass) att_cp16(vd + kk * ATT_MMA_LD + c8 * 8, vb + off, ok);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    stage(0);
     for (int i = tid; i < ATT_MMA_ROWS * (FA_HEAD_DIM / 8); i += 256) {
         const int r = i / (FA_HEAD_DIM / 8), c8 = i % (FA_HEAD_DIM / 8), t = q0 + r / FA_GQA;
         uint4 v = make_uint4(0, 0, 0, 0);
         if (t < S) v = *reinterpret_cast<const uint4*>(q + (size_t)t * FA_Q_SIZE + (kvh * FA_GQA + r % FA_GQA) * FA_HEAD_DIM + c8 * 8);
         *reinterpret_cast<uint4*>(Qs + r * ATT_MMA_LD + c8 * 8) = v;
     }
-    const int t_last = min(q0 + ATT_MMA_Q, S) - 1;
-    const int nchunks = t_last / ATT_MMA_KEYS + 1;
     const int r0 = warp * 16 + g, r1 = r0 + 8;                     // this thread's two rows
     const int t0 = q0 + r0 / FA_GQA, t1 = q0 + r1 / FA_GQA;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
@@ -809,21 +828,15 @@ static __global__ void __launch_bounds__(256, 1) pf_attention_mma_kernel(const b
 #pragma unroll
     for (int nt = 0; nt < FA_HEAD_DIM / 8; ++nt) { o[nt][0] = 0.f; o[nt][1] = 0.f; o[nt][2] = 0.f; o[nt][3] = 0.f; }
 
-    for (int pass = 0; pass < 2; ++pass) {
-        for (int ch = 0; ch < nchunks; ++ch) {
+    {
+        for (int item = 0; item < nitems; ++item) {
+            const int pass = item >= nchunks, ch = pass ? item - nchunks : item;
             const int j0 = ch * ATT_MMA_KEYS;
-            __syncthreads();
-            for (int i = tid; i < ATT_MMA_KEYS * (FA_HEAD_DIM / 8); i += 256) {
-                const int kk = i / (FA_HEAD_DIM / 8), c8 = i % (FA_HEAD_DIM / 8);
-                uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-                if (j0 + kk < S) {
-                    kv = *reinterpret_cast<const uint4*>(kb + (size_t)(j0 + kk) * FA_HEAD_DIM + c8 * 8);
-                    if (pass) vv = *reinterpret_cast<const uint4*>(vb + (size_t)(j0 + kk) * FA_HEAD_DIM + c8 * 8);
-                }
-                *reinterpret_cast<uint4*>(Ks + kk * ATT_MMA_LD + c8 * 8) = kv;
-                if (pass) *reinterpret_cast<uint4*>(Vs + kk * ATT_MMA_LD + c8 * 8) = vv;
-            }
-            __syncthreads();
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+            __syncthreads();                                      // this item's chunk (and Q) is in; everybody is done with the previous one
+            if (item + 1 < nitems) stage(item + 1);
+            const bf16* Ks = KV + (size_t)(item & 1) * 2 * ATT_MMA_KEYS * ATT_MMA_LD;
+            const bf16* Vs = Ks + ATT_MMA_KEYS * ATT_MMA_LD;
             // scores of this warp's 16 rows against the 64 keys
             float sacc[ATT_MMA_KEYS / 8][4];
 #pragma unroll
