@@ -708,6 +708,21 @@ bool make_tmap(CUtensorMap* tm, const void* ptr, int rows, int cols, int ld, int
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// bf16 tensor of rank 2 or 3 (dims innermost first, strides in bytes for dims 1..), 128-byte swizzle: the inner box extent
+// must be 64 elements.  Used by the attention kernels for their Q / K / V^T boxes.
+bool make_tmap_bf16(CUtensorMap* tm, const void* ptr, int rank, const unsigned long long* dims, const unsigned long long* strides_bytes,
+                    const unsigned* box) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || rank < 2 || rank > 3) return false;
+    cuuint64_t d[3], st[2];
+    cuuint32_t b[3], estr[3] = {1, 1, 1};
+    for (int i = 0; i < rank; ++i) { d[i] = dims[i]; b[i] = box[i]; }
+    for (int i = 0; i + 1 < rank; ++i) st[i] = strides_bytes[i];
+    return fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (cuuint32_t)rank, const_cast<void*>(ptr), d, st, b, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Q4_K super-blocks as a 2-D byte tensor [rows][K/256 * 144]; box = one super-block (144 bytes) x 64 rows, no swizzle.
 static bool make_tmap_q4k(CUtensorMap* tm, const void* ptr, int rows, int K) {
     EncodeTiledFn fn = encode_fn();

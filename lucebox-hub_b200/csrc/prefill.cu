@@ -20,6 +20,9 @@ namespace q35 {
 int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ldc, const bf16* R, int ldr,
               int M, int N, int K, int epi, int up_row_offset, cudaStream_t stream);
 int quantize_act_nvfp4(const bf16* x, int tokens, int K, void* packed_out, void* scales_out, cudaStream_t stream);
+size_t attention_tcgen05_scratch_bytes(int S);
+int attention_prefill_tcgen05(const bf16* q, const bf16* k_cache, const bf16* v_cache, const bf16* proj, int ldp, bf16* out, bf16* vt_scratch, int S,
+                              int max_seq, cudaStream_t stream);
 int gemm_nvfp4(const void* a_packed, const void* a_scales, int tokens, const void* w_packed, const void* w_scales, int n_rows, int n_out, int K,
                float alpha, void* C, int ldc, int out_f32, const bf16* R, int ldr, cudaStream_t stream);
 
@@ -71,8 +74,6 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
     if (attr_done.pending()) {
         Q35_CUDA_OK(cudaFuncSetAttribute(pf_dn_chunk_local_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CHUNK_LOCAL_SMEM));
         Q35_CUDA_OK(cudaFuncSetAttribute(pf_dn_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CHUNK_SCAN_SMEM));
-        Q35_CUDA_OK(cudaFuncSetAttribute(pf_attention_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_MMA_SMEM));
-        Q35_CUDA_OK(cudaFuncSetAttribute(pf_attention_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ATS_SMEM));
         attr_done.mark();
     }
     const int nchunks = (S + DN_CHUNK - 1) / DN_CHUNK;
@@ -83,12 +84,14 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
     const size_t chunk_bytes = ((size_t)DN_HEADS * nchunks * sizeof(ChunkScratch) + 255) & ~(size_t)255;
     const size_t tpad = ((size_t)S + 127) / 128 * 128;
     const size_t act_packed_bytes = tpad * (HIDDEN / 2), act_scale_bytes = tpad / 128 * (HIDDEN / 64) * 512;
-    char* scratch_base = (char*)get_scratch(chunk_bytes + act_packed_bytes + act_scale_bytes + (size_t)VOCAB * 2 + 256);
+    const size_t head_bytes = (chunk_bytes + act_packed_bytes + act_scale_bytes + (size_t)VOCAB * 2 + 256 + 1023) & ~(size_t)1023;
+    char* scratch_base = (char*)get_scratch(head_bytes + attention_tcgen05_scratch_bytes(S) + 1024);
     if (!scratch_base) return QWEN35_ERR_CUDA;
     ChunkScratch* scratch = (ChunkScratch*)scratch_base;
     uint8_t* act_packed = (uint8_t*)scratch_base + chunk_bytes;
     uint8_t* act_scales = act_packed + act_packed_bytes;
     bf16* lm_logits = (bf16*)(act_scales + ((act_scale_bytes + 255) & ~(size_t)255));
+    bf16* vt_scratch = (bf16*)(((uintptr_t)scratch_base + head_bytes + 1023) & ~(uintptr_t)1023);     // V^T of the attention layer in flight
     RopeTable rt;
     for (int i = 0; i < FA_ROT / 2; ++i) rt.f[i] = 1.0f / (float)std::pow(1.0e7, (double)((float)(2 * i) / (float)FA_ROT));
 
@@ -150,13 +153,8 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
             bf16* vc = a.v_cache + (size_t)i_fa * FA_KV_HEADS * a.max_seq_len * FA_HEAD_DIM;
             Q35_CUDA_OK(pdl_launch(pf_qk_norm_rope_kernel, (S * 12 + 7) / 8, 256, 0, stream, a.proj_buf, ldp, (const bf16*)L.p[FA_QNORM], (const bf16*)L.p[FA_KNORM], rt,
                                                                          a.proj_buf2, kc, vc, S, a.max_seq_len));
-            if (S <= ATS_MAX_S)
-                Q35_CUDA_OK(pdl_launch(pf_attention_split_kernel, dim3((S + ATS_Q - 1) / ATS_Q, FA_KV_HEADS), 256, ATS_SMEM, stream,
-                    a.proj_buf2, kc, vc, a.proj_buf, ldp, a.attn_buf, S, a.max_seq_len));
-            else
-                Q35_CUDA_OK(pdl_launch(pf_attention_mma_kernel, dim3((S + ATT_MMA_Q - 1) / ATT_MMA_Q, FA_KV_HEADS), 256, ATT_MMA_SMEM, stream,
-                    a.proj_buf2, kc, vc, a.proj_buf, ldp, a.attn_buf, S, a.max_seq_len));
-            g_launches.fetch_add(2);
+            Q35_TRY(attention_prefill_tcgen05(a.proj_buf2, kc, vc, a.proj_buf, ldp, a.attn_buf, vt_scratch, S, a.max_seq_len, stream));
+            g_launches.fetch_add(1);
             w_out = (const bf16*)L.p[FA_O]; w_post = (const bf16*)L.p[FA_POST_NORM]; w_down = (const bf16*)L.p[FA_DOWN];
             ++i_fa;
         }

@@ -769,345 +769,6 @@ static __global__ void __launch_bounds__(256) pf_qk_norm_rope_kernel(const bf16*
 
 constexpr int ATT_PF_MAX_S = 4096;      // longest prompt the prefill entry points accept
 
-// ---- causal GQA attention on tensor cores (mma.sync m16n8k16 bf16) ------------------------------------------
-// Rounding points of the bf16 HuggingFace model: scores = bf16(q.k)/16, softmax in f32 over the whole row, P rounded to
-// bf16, out = bf16(P.V), times bf16(sigmoid(gate)).
-// One CTA = 32 queries x the 4 q heads of one kv head = 128 rows (row r: query r/4, head r%4), one 16-row tile per
-// warp, so a K/V chunk staged in shared memory serves all four heads.  Exact softmax in two passes over the causal
-// key range: pass 1 the running row maximum and normaliser from bf16(q.k)/16; pass 2 recomputes the same scores (same
-// instructions, same values), forms P = bf16(exp(s - m) / l) in registers (the accumulator layout of two adjacent
-// 8-key tiles is the A-operand layout of a 16-key step) and accumulates P.V.  Fragments come from ldmatrix on rows
-// padded to 528 bytes (conflict-free); V is read with ldmatrix.trans.  K (and V in pass 2) chunks arrive by cp.async into
-// two buffers: the next chunk's copies fly while this one is computed on, one __syncthreads per chunk.
-constexpr int ATT_MMA_Q = 32, ATT_MMA_ROWS = ATT_MMA_Q * FA_GQA, ATT_MMA_KEYS = 64, ATT_MMA_LD = FA_HEAD_DIM + 8;
-constexpr int ATT_MMA_SMEM = (ATT_MMA_ROWS + 4 * ATT_MMA_KEYS) * ATT_MMA_LD * 2;      // Q tile + two (K, V) chunk buffers
-
-__device__ __forceinline__ void att_cp16(bf16* dst, const bf16* src, bool valid) {
-    const int n = valid ? 16 : 0;        // 0 source bytes: the 16 destination bytes are zero-filled
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src), "r"(n) : "memory");
-}
-
-static __global__ void __launch_bounds__(256, 1) pf_attention_mma_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k_cache,
-                                                                  const bf16* __restrict__ v_cache, const bf16* __restrict__ proj, int ldp,
-                                                                  bf16* __restrict__ out, int S, int max_seq) {
-    pdl_wait();
-    extern __shared__ __align__(16) unsigned char att_mma_sm[];
-    bf16* Qs = reinterpret_cast<bf16*>(att_mma_sm);
-    bf16* KV = Qs + ATT_MMA_ROWS * ATT_MMA_LD;                    // [buffer 2][K, V][64][LD]
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
-    const int blk = (int)gridDim.x - 1 - (int)blockIdx.x;          // long blocks first
-    const int kvh = blockIdx.y, q0 = blk * ATT_MMA_Q;
-    const bf16* kb = k_cache + (size_t)kvh * max_seq * FA_HEAD_DIM;
-    const bf16* vb = v_cache + (size_t)kvh * max_seq * FA_HEAD_DIM;
-    const int t_last = min(q0 + ATT_MMA_Q, S) - 1;
-    const int nchunks = t_last / ATT_MMA_KEYS + 1, nitems = 2 * nchunks;
-    auto stage = [&](int item) {
-        const int pass = item >= nchunks, j0 = (pass ? item - nchunks : item) * ATT_MMA_KEYS;
-        bf16* kd = KV + (size_t)(item & 1) * 2 * ATT_MMA_KEYS * ATT_MMA_LD;
-        bf16* vd = kd + ATT_MMA_KEYS * ATT_MMA_LD;
-        for (int i = tid; i < ATT_MMA_KEYS * (FA_HEAD_DIM / 8); i += 256) {
-            const int kk = i / (FA_HEAD_DIM / 8), c8 = i % (FA_HEAD_DIM / 8);
-            const bool ok = j0 + kk < S;
-            const size_t off = (size_t)(ok ? j0 + kk : 0) * FA_HEAD_DIM + c8 * 8;
-            att_cp16(kd + kk * ATT_MMA_LD + c8 * 8, kb + off, ok);
-            if (pass) att_cp16(vd + kk * ATT_MMA_LD + c8 * 8, vb + off, ok);
-        }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-    };
-    stage(0);
-    for (int i = tid; i < ATT_MMA_ROWS * (FA_HEAD_DIM / 8); i += 256) {
-        const int r = i / (FA_HEAD_DIM / 8), c8 = i % (FA_HEAD_DIM / 8), t = q0 + r / FA_GQA;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (t < S) v = *reinterpret_cast<const uint4*>(q + (size_t)t * FA_Q_SIZE + (kvh * FA_GQA + r % FA_GQA) * FA_HEAD_DIM + c8 * 8);
-        *reinterpret_cast<uint4*>(Qs + r * ATT_MMA_LD + c8 * 8) = v;
-    }
-    const int r0 = warp * 16 + g, r1 = r0 + 8;                     // this thread's two rows
-    const int t0 = q0 + r0 / FA_GQA, t1 = q0 + r1 / FA_GQA;
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    float o[FA_HEAD_DIM / 8][4];
-#pragma unroll
-    for (int nt = 0; nt < FA_HEAD_DIM / 8; ++nt) { o[nt][0] = 0.f; o[nt][1] = 0.f; o[nt][2] = 0.f; o[nt][3] = 0.f; }
-
-    {
-        for (int item = 0; item < nitems; ++item) {
-            const int pass = item >= nchunks, ch = pass ? item - nchunks : item;
-            const int j0 = ch * ATT_MMA_KEYS;
-            asm volatile("cp.async.wait_group 0;" ::: "memory");
-            __syncthreads();                                      // this item's chunk (and Q) is in; everybody is done with the previous one
-            if (item + 1 < nitems) stage(item + 1);
-            const bf16* Ks = KV + (size_t)(item & 1) * 2 * ATT_MMA_KEYS * ATT_MMA_LD;
-            const bf16* Vs = Ks + ATT_MMA_KEYS * ATT_MMA_LD;
-            // scores of this warp's 16 rows against the 64 keys
-            float sacc[ATT_MMA_KEYS / 8][4];
-#pragma unroll
-            for (int nt = 0; nt < ATT_MMA_KEYS / 8; ++nt) { sacc[nt][0] = 0.f; sacc[nt][1] = 0.f; sacc[nt][2] = 0.f; sacc[nt][3] = 0.f; }
-#pragma unroll 4
-            for (int ks = 0; ks < FA_HEAD_DIM / 16; ++ks) {
-                uint32_t a[4];
-                ldsm_x4(a, Qs + (warp * 16 + (lane & 15)) * ATT_MMA_LD + ks * 16 + (lane >> 4) * 8);
-#pragma unroll
-                for (int np = 0; np < ATT_MMA_KEYS / 16; ++np) {
-                    uint32_t b[4];
-                    ldsm_x4(b, Ks + (np * 16 + (lane & 7) + 8 * (lane >> 4)) * ATT_MMA_LD + ks * 16 + 8 * ((lane >> 3) & 1));
-                    mma_16816(sacc[2 * np], a, b[0], b[1]);
-                    mma_16816(sacc[2 * np + 1], a, b[2], b[3]);
-                }
-            }
-            // bf16 rounding, scale, causal mask
-#pragma unroll
-            for (int nt = 0; nt < ATT_MMA_KEYS / 8; ++nt)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int j = j0 + nt * 8 + 2 * c + (e & 1);
-                    const int tr = (e < 2) ? t0 : t1;
-                    sacc[nt][e] = (j <= tr && tr < S) ? rbf(sacc[nt][e]) * 0.0625f : -INFINITY;
-                }
-            if (pass == 0) {
-                float cm0 = -INFINITY, cm1 = -INFINITY;
-#pragma unroll
-                for (int nt = 0; nt < ATT_MMA_KEYS / 8; ++nt) {
-                    cm0 = fmaxf(cm0, fmaxf(sacc[nt][0], sacc[nt][1]));
-                    cm1 = fmaxf(cm1, fmaxf(sacc[nt][2], sacc[nt][3]));
-                }
-                cm0 = fmaxf(cm0, __shfl_xor_sync(0xffffffffu, cm0, 1)); cm0 = fmaxf(cm0, __shfl_xor_sync(0xffffffffu, cm0, 2));
-                cm1 = fmaxf(cm1, __shfl_xor_sync(0xffffffffu, cm1, 1)); cm1 = fmaxf(cm1, __shfl_xor_sync(0xffffffffu, cm1, 2));
-                const float n0 = fmaxf(m0, cm0), n1 = fmaxf(m1, cm1);
-                float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-                for (int nt = 0; nt < ATT_MMA_KEYS / 8; ++nt) {
-                    if (n0 != -INFINITY) s0 += expf(sacc[nt][0] - n0) + expf(sacc[nt][1] - n0);
-                    if (n1 != -INFINITY) s1 += expf(sacc[nt][2] - n1) + expf(sacc[nt][3] - n1);
-                }
-                s0 += __shfl_xor_sync(0xffffffffu, s0, 1); s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
-                s1 += __shfl_xor_sync(0xffffffffu, s1, 1); s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-                l0 = (m0 == -INFINITY ? 0.f : l0 * expf(m0 - n0)) + s0;
-                l1 = (m1 == -INFINITY ? 0.f : l1 * expf(m1 - n1)) + s1;
-                m0 = n0; m1 = n1;
-            } else {
-                // P in A-operand layout, then P.V
-#pragma unroll
-                for (int ks = 0; ks < ATT_MMA_KEYS / 16; ++ks) {
-                    uint32_t a[4];
-#pragma unroll
-                    for (int hf = 0; hf < 2; ++hf) {
-                        const float* sv = sacc[2 * ks + hf];
-                        const float p00 = (sv[0] == -INFINITY) ? 0.f : expf(sv[0] - m0) / l0, p01 = (sv[1] == -INFINITY) ? 0.f : expf(sv[1] - m0) / l0;
-                        const float p10 = (sv[2] == -INFINITY) ? 0.f : expf(sv[2] - m1) / l1, p11 = (sv[3] == -INFINITY) ? 0.f : expf(sv[3] - m1) / l1;
-                        const __nv_bfloat162 x0 = __floats2bfloat162_rn(p00, p01), x1 = __floats2bfloat162_rn(p10, p11);
-                        a[2 * hf] = *reinterpret_cast<const uint32_t*>(&x0);
-                        a[2 * hf + 1] = *reinterpret_cast<const uint32_t*>(&x1);
-                    }
-#pragma unroll
-                    for (int np = 0; np < FA_HEAD_DIM / 16; ++np) {
-                        uint32_t b[4];
-                        ldsm_x4_trans(b, Vs + (ks * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * ATT_MMA_LD + np * 16 + 8 * (lane >> 4));
-                        mma_16816(o[2 * np], a, b[0], b[1]);
-                        mma_16816(o[2 * np + 1], a, b[2], b[3]);
-                    }
-                }
-            }
-        }
-    }
-    // output: bf16(P.V) * bf16(sigmoid(gate)), rows r0 (o[.][0..1]) and r1 (o[.][2..3])
-#pragma unroll
-    for (int hf = 0; hf < 2; ++hf) {
-        const int r = hf ? r1 : r0, t = hf ? t1 : t0;
-        if (t >= S) continue;
-        const int head = kvh * FA_GQA + r % FA_GQA;
-        const bf16* gate = proj + (size_t)t * ldp + head * 2 * FA_HEAD_DIM + FA_HEAD_DIM;
-        bf16* dst = out + (size_t)t * FA_Q_SIZE + head * FA_HEAD_DIM;
-#pragma unroll
-        for (int nt = 0; nt < FA_HEAD_DIM / 8; ++nt) {
-            const int d = nt * 8 + 2 * c;
-            const uint32_t gr = *reinterpret_cast<const uint32_t*>(gate + d);
-            const __nv_bfloat162 pr = __halves2bfloat162(f2bf(rbf(o[nt][2 * hf]) * rbf(sigmoid_f(bf_lo(gr)))), f2bf(rbf(o[nt][2 * hf + 1]) * rbf(sigmoid_f(bf_hi(gr)))));
-            *reinterpret_cast<__nv_bfloat162*>(dst + d) = pr;
-        }
-    }
-}
-
-// ---- the same attention for short prompts: keys of a chunk split over four warps -------------------------------
-// With few query blocks the kernel above leaves most SMs idle and each warp walks the whole key range alone.  Here a CTA takes
-// 8 queries x 4 heads = 32 rows (two 16-row tiles) and 8 warps = (row tile rt, key quarter ks): per 64-key chunk a warp
-// computes the scores of its 16 keys only (its Q fragments stay in registers), so the chain per chunk is a quarter as long
-// and S / 8 x 2 CTAs fill the machine at S ~ 500.  Pass 1 gives each warp the maximum and normaliser of its keys; the four
-// partial pairs of a row tile are merged through shared memory.  In pass 2 each warp rounds its P = bf16(exp(s - m) / l)
-// values (the same rounding points as above) into a shared [16 x 64] tile, and after a barrier of the row tile's four
-// warps each accumulates P.V for its own quarter of the head dimension, so no partial outputs have to be summed.
-// K (and V in pass 2) chunks arrive by cp.async into two buffers, one __syncthreads per chunk.
-constexpr int ATS_Q = 8, ATS_ROWS = ATS_Q * FA_GQA, ATS_KEYS = 64, ATS_LD = FA_HEAD_DIM + 8, ATS_PLD = ATS_KEYS + 8;
-constexpr int ATS_SMEM = (ATS_ROWS * ATS_LD + 4 * ATS_KEYS * ATS_LD + 2 * 16 * ATS_PLD) * 2 + 2 * 4 * 16 * 2 * 4;
-constexpr int ATS_MAX_S = 1024;          // longer prompts have enough query blocks for the kernel above, which re-reads K / V less
-
-__device__ __forceinline__ void ats_cp16(bf16* dst, const bf16* src, bool valid) {
-    const int n = valid ? 16 : 0;        // 0 source bytes: the 16 destination bytes are zero-filled
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src), "r"(n) : "memory");
-}
-
-static __global__ void __launch_bounds__(256, 1) pf_attention_split_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k_cache,
-                                                                    const bf16* __restrict__ v_cache, const bf16* __restrict__ proj, int ldp,
-                                                                    bf16* __restrict__ out, int S, int max_seq) {
-    pdl_wait();
-    extern __shared__ __align__(16) unsigned char ats_sm[];
-    bf16* Qs = reinterpret_cast<bf16*>(ats_sm);
-    bf16* KV = Qs + ATS_ROWS * ATS_LD;                    // [buffer 2][K, V][64][LD]
-    bf16* Ps = KV + 4 * ATS_KEYS * ATS_LD;                // [row tile 2][16][PLD]
-    float* ML = reinterpret_cast<float*>(Ps + 2 * 16 * ATS_PLD);   // [row tile 2][ks 4][16 rows][m, l]
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
-    const int rt = warp >> 2, ks = warp & 3;
-    const int blk = (int)gridDim.x - 1 - (int)blockIdx.x;          // long blocks first
-    const int kvh = blockIdx.y, q0 = blk * ATS_Q;
-    const bf16* kb = k_cache + (size_t)kvh * max_seq * FA_HEAD_DIM;
-    const bf16* vb = v_cache + (size_t)kvh * max_seq * FA_HEAD_DIM;
-    const int t_last = min(q0 + ATS_Q, S) - 1;
-    const int nchunks = t_last / ATS_KEYS + 1, nitems = 2 * nchunks;
-
-    auto stage = [&](int item) {
-        const int pass = item >= nchunks, j0 = (pass ? item - nchunks : item) * ATS_KEYS;
-        bf16* kd = KV + (size_t)(item & 1) * 2 * ATS_KEYS * ATS_LD;
-        bf16* vd = kd + ATS_KEYS * ATS_LD;
-        for (int i = tid; i < ATS_KEYS * (FA_HEAD_DIM / 8); i += 256) {
-            const int kk = i / (FA_HEAD_DIM / 8), c8 = i % (FA_HEAD_DIM / 8);
-            const bool ok = j0 + kk < S;
-            const size_t off = (size_t)(ok ? j0 + kk : 0) * FA_HEAD_DIM + c8 * 8;
-            ats_cp16(kd + kk * ATS_LD + c8 * 8, kb + off, ok);
-            if (pass) ats_cp16(vd + kk * ATS_LD + c8 * 8, vb + off, ok);
-        }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-    };
-
-    stage(0);
-    for (int i = tid; i < ATS_ROWS * (FA_HEAD_DIM / 8); i += 256) {
-        const int r = i / (FA_HEAD_DIM / 8), c8 = i % (FA_HEAD_DIM / 8), t = q0 + r / FA_GQA;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (t < S) v = *reinterpret_cast<const uint4*>(q + (size_t)t * FA_Q_SIZE + (kvh * FA_GQA + r % FA_GQA) * FA_HEAD_DIM + c8 * 8);
-        *reinterpret_cast<uint4*>(Qs + r * ATS_LD + c8 * 8) = v;
-    }
-    __syncthreads();
-    uint32_t qf[FA_HEAD_DIM / 16][4];
-#pragma unroll
-    for (int kk = 0; kk < FA_HEAD_DIM / 16; ++kk) ldsm_x4(qf[kk], Qs + (rt * 16 + (lane & 15)) * ATS_LD + kk * 16 + (lane >> 4) * 8);
-
-    const int r0 = rt * 16 + g, r1 = r0 + 8;                       // this thread's two rows
-    const int t0 = q0 + r0 / FA_GQA, t1 = q0 + r1 / FA_GQA;
-    const int t_max_rt = min(q0 + (rt * 16 + 15) / FA_GQA, S - 1);  // last query of this row tile
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    float o[8][4];
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) { o[nt][0] = 0.f; o[nt][1] = 0.f; o[nt][2] = 0.f; o[nt][3] = 0.f; }
-    bf16* Pt = Ps + rt * 16 * ATS_PLD;
-
-    for (int item = 0; item < nitems; ++item) {
-        const int pass = item >= nchunks, j0 = (pass ? item - nchunks : item) * ATS_KEYS;
-        asm volatile("cp.async.wait_group 0;" ::: "memory");
-        if (item == nchunks) {                                    // end of pass 1: publish this warp's (m, l) before the barrier
-            if (c == 0) {
-                float* d = ML + ((rt * 4 + ks) * 16) * 2;
-                d[2 * g] = m0; d[2 * g + 1] = l0; d[2 * (g + 8)] = m1; d[2 * (g + 8) + 1] = l1;
-            }
-        }
-        __syncthreads();                                          // this item's chunk is in; every warp is done with the previous one
-        if (item + 1 < nitems) stage(item + 1);
-        if (item == nchunks) {                                    // merge the four key quarters' partial softmax statistics
-            float M0 = -INFINITY, M1 = -INFINITY;
-#pragma unroll
-            for (int k2 = 0; k2 < 4; ++k2) {
-                const float* d = ML + ((rt * 4 + k2) * 16) * 2;
-                M0 = fmaxf(M0, d[2 * g]); M1 = fmaxf(M1, d[2 * (g + 8)]);
-            }
-            float L0 = 0.f, L1 = 0.f;
-#pragma unroll
-            for (int k2 = 0; k2 < 4; ++k2) {
-                const float* d = ML + ((rt * 4 + k2) * 16) * 2;
-                if (d[2 * g] != -INFINITY) L0 += d[2 * g + 1] * expf(d[2 * g] - M0);
-                if (d[2 * (g + 8)] != -INFINITY) L1 += d[2 * (g + 8) + 1] * expf(d[2 * (g + 8)] - M1);
-            }
-            m0 = M0; m1 = M1; l0 = L0; l1 = L1;
-        }
-        if (j0 > t_max_rt) continue;                              // chunk beyond this row tile's causal range (uniform per row tile)
-        const bf16* Kc = KV + (size_t)(item & 1) * 2 * ATS_KEYS * ATS_LD;
-        const bf16* Vc = Kc + ATS_KEYS * ATS_LD;
-        // scores of the 16 rows against this warp's 16 keys
-        float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-        const bool live = j0 + ks * 16 <= t_max_rt;               // any unmasked key in this quarter
-        if (live) {
-#pragma unroll
-            for (int kk = 0; kk < FA_HEAD_DIM / 16; ++kk) {
-                uint32_t b[4];
-                ldsm_x4(b, Kc + (ks * 16 + (lane & 7) + 8 * (lane >> 4)) * ATS_LD + kk * 16 + 8 * ((lane >> 3) & 1));
-                mma_16816(sacc[0], qf[kk], b[0], b[1]);
-                mma_16816(sacc[1], qf[kk], b[2], b[3]);
-            }
-        }
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int j = j0 + ks * 16 + nt * 8 + 2 * c + (e & 1);
-                const int tr = (e < 2) ? t0 : t1;
-                sacc[nt][e] = (live && j <= tr && tr < S) ? rbf(sacc[nt][e]) * 0.0625f : -INFINITY;
-            }
-        if (!pass) {
-            float cm0 = fmaxf(fmaxf(sacc[0][0], sacc[0][1]), fmaxf(sacc[1][0], sacc[1][1]));
-            float cm1 = fmaxf(fmaxf(sacc[0][2], sacc[0][3]), fmaxf(sacc[1][2], sacc[1][3]));
-            cm0 = fmaxf(cm0, __shfl_xor_sync(0xffffffffu, cm0, 1)); cm0 = fmaxf(cm0, __shfl_xor_sync(0xffffffffu, cm0, 2));
-            cm1 = fmaxf(cm1, __shfl_xor_sync(0xffffffffu, cm1, 1)); cm1 = fmaxf(cm1, __shfl_xor_sync(0xffffffffu, cm1, 2));
-            const float n0 = fmaxf(m0, cm0), n1 = fmaxf(m1, cm1);
-            float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-                if (n0 != -INFINITY) s0 += expf(sacc[nt][0] - n0) + expf(sacc[nt][1] - n0);
-                if (n1 != -INFINITY) s1 += expf(sacc[nt][2] - n1) + expf(sacc[nt][3] - n1);
-            }
-            s0 += __shfl_xor_sync(0xffffffffu, s0, 1); s0 += __shfl_xor_sync(0xffffffffu, s0, 2);
-            s1 += __shfl_xor_sync(0xffffffffu, s1, 1); s1 += __shfl_xor_sync(0xffffffffu, s1, 2);
-            l0 = (m0 == -INFINITY ? 0.f : l0 * expf(m0 - n0)) + s0;
-            l1 = (m1 == -INFINITY ? 0.f : l1 * expf(m1 - n1)) + s1;
-            m0 = n0; m1 = n1;
-        } else {
-            // P of this warp's 16 keys into the row tile's shared [16 x 64] tile
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-                const float* sv = sacc[nt];
-                const float p00 = (sv[0] == -INFINITY) ? 0.f : expf(sv[0] - m0) / l0, p01 = (sv[1] == -INFINITY) ? 0.f : expf(sv[1] - m0) / l0;
-                const float p10 = (sv[2] == -INFINITY) ? 0.f : expf(sv[2] - m1) / l1, p11 = (sv[3] == -INFINITY) ? 0.f : expf(sv[3] - m1) / l1;
-                *reinterpret_cast<__nv_bfloat162*>(Pt + g * ATS_PLD + ks * 16 + nt * 8 + 2 * c) = __floats2bfloat162_rn(p00, p01);
-                *reinterpret_cast<__nv_bfloat162*>(Pt + (g + 8) * ATS_PLD + ks * 16 + nt * 8 + 2 * c) = __floats2bfloat162_rn(p10, p11);
-            }
-            asm volatile("bar.sync %0, 128;" ::"r"(1 + rt) : "memory");      // the four warps of this row tile
-            // P.V for head dimensions [64 ks, 64 ks + 64)
-            const int nk = min(4, (t_max_rt - j0) / 16 + 1);      // 16-key steps with any unmasked key
-            for (int k2 = 0; k2 < nk; ++k2) {
-                uint32_t a[4];
-                ldsm_x4(a, Pt + (lane & 15) * ATS_PLD + k2 * 16 + (lane >> 4) * 8);
-#pragma unroll
-                for (int np = 0; np < 4; ++np) {
-                    uint32_t b[4];
-                    ldsm_x4_trans(b, Vc + (k2 * 16 + (lane & 7) + 8 * ((lane >> 3) & 1)) * ATS_LD + ks * 64 + np * 16 + 8 * (lane >> 4));
-                    mma_16816(o[2 * np], a, b[0], b[1]);
-                    mma_16816(o[2 * np + 1], a, b[2], b[3]);
-                }
-            }
-        }
-    }
-    // output: bf16(P.V) * bf16(sigmoid(gate)), rows r0 (o[.][0..1]) and r1 (o[.][2..3]), this warp's 64 head dimensions
-#pragma unroll
-    for (int hf = 0; hf < 2; ++hf) {
-        const int r = hf ? r1 : r0, t = hf ? t1 : t0;
-        if (t >= S) continue;
-        const int head = kvh * FA_GQA + r % FA_GQA;
-        const bf16* gate = proj + (size_t)t * ldp + head * 2 * FA_HEAD_DIM + FA_HEAD_DIM;
-        bf16* dst = out + (size_t)t * FA_Q_SIZE + head * FA_HEAD_DIM;
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-            const int d = ks * 64 + nt * 8 + 2 * c;
-            const uint32_t gr = *reinterpret_cast<const uint32_t*>(gate + d);
-            const __nv_bfloat162 pr = __halves2bfloat162(f2bf(rbf(o[nt][2 * hf]) * rbf(sigmoid_f(bf_lo(gr)))), f2bf(rbf(o[nt][2 * hf + 1]) * rbf(sigmoid_f(bf_hi(gr)))));
-            *reinterpret_cast<__nv_bfloat162*>(dst + d) = pr;
-        }
-    }
-}
-
 // ---- last-token LM head: GEMV over the vocabulary + arg-max (lowest index among equal bf16 maxima) -----
 static __global__ void __launch_bounds__(256) pf_lm_head_kernel(const bf16* __restrict__ x, const bf16* __restrict__ lm, float* __restrict__ bmv,
                                                          int* __restrict__ bmi, float* __restrict__ logits_out) {
