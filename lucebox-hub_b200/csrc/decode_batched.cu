@@ -52,6 +52,14 @@ __global__ void __launch_bounds__(256) bd_dn_step_kernel(const bf16* __restrict_
     const int b = blockIdx.x, h = blockIdx.y, rb = blockIdx.z, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bf16* xrow = proj + (size_t)b * ldp;
     const float4* cv = reinterpret_cast<const float4*>(conv + (size_t)b * conv_seq_stride);
+    // this warp's state rows first: they depend on nothing computed here, so they stream in while q, k, v, beta and the decay
+    // are prepared (the kernel is bound by these 134 MB per launch)
+    float* st_base = state + (size_t)b * state_seq_stride + (size_t)h * DN_V * DN_K;
+    constexpr int RPW = BD_DN_ROWS / 8;                 // rows per warp
+    float4 t[RPW];
+#pragma unroll
+    for (int r = 0; r < RPW; ++r)
+        t[r] = __ldcs(reinterpret_cast<const float4*>(st_base + (size_t)(rb * BD_DN_ROWS + warp * RPW + r) * DN_K) + lane);
     // q (threads 0-127) and k (threads 128-255) of this head: conv + SiLU, then the L2 norm in bf16 arithmetic
     const int which = tid >> 7, i = tid & 127;
     const int chx = which * DN_QK_SIZE + h * DN_K + i;
@@ -81,12 +89,6 @@ __global__ void __launch_bounds__(256) bd_dn_step_kernel(const bf16* __restrict_
     const float4 q4 = *reinterpret_cast<const float4*>(&sqk[0][lane * 4]);
     const float4 k4 = *reinterpret_cast<const float4*>(&sqk[1][lane * 4]);
     const float beta = shd[0], decay = shd[1];
-    float* st_base = state + (size_t)b * state_seq_stride + (size_t)h * DN_V * DN_K;
-    constexpr int RPW = BD_DN_ROWS / 8;                 // rows per warp
-    float4 t[RPW];
-#pragma unroll
-    for (int r = 0; r < RPW; ++r)
-        t[r] = *(reinterpret_cast<const float4*>(st_base + (size_t)(rb * BD_DN_ROWS + warp * RPW + r) * DN_K) + lane);
 #pragma unroll
     for (int r = 0; r < RPW; ++r) {
         const int vl = warp * RPW + r, v = rb * BD_DN_ROWS + vl;
@@ -99,7 +101,7 @@ __global__ void __launch_bounds__(256) bd_dn_step_kernel(const bf16* __restrict_
         u.z = __fadd_rn(u.z, __fmul_rn(k4.z, delta)); u.w = __fadd_rn(u.w, __fmul_rn(k4.w, delta));
         float o = __fadd_rn(__fadd_rn(__fadd_rn(__fmul_rn(u.x, q4.x), __fmul_rn(u.y, q4.y)), __fmul_rn(u.z, q4.z)), __fmul_rn(u.w, q4.w));
         o = warp_sum(o);
-        *(reinterpret_cast<float4*>(st_base + (size_t)v * DN_K) + lane) = u;
+        __stcs(reinterpret_cast<float4*>(st_base + (size_t)v * DN_K) + lane, u);
         if (lane == 0) core_out[(size_t)b * DN_V_SIZE + h * DN_V + v] = f2bf(o);
     }
 }
@@ -219,7 +221,7 @@ __global__ void __launch_bounds__(128) bd_att_scores_kernel(const __grid_constan
                                                             float* __restrict__ scores, float* __restrict__ stats, int max_ctx, int max_slices,
                                                             int* __restrict__ status) {
     extern __shared__ unsigned char bd_sm_raw[];
-    __shared__ float ssc[FA_GQA][BD_CHUNK];
+    __shared__ float ssc[2][FA_GQA][BD_CHUNK];           // scores of a page, double buffered: one barrier per page
     __shared__ int spg[BD_MAX_PAGES_SLICE];
     __shared__ __align__(8) u64 bars[BD_NBUF];
     const uint32_t raw = smem_u32(bd_sm_raw), pages_s = (raw + 1023u) & ~1023u;      // swizzled boxes need 1024-byte alignment
@@ -249,6 +251,10 @@ __global__ void __launch_bounds__(128) bd_att_scores_kernel(const __grid_constan
         bd_issue_page(&tmK, spg[0], kvh, pages_s, smem_u32(&bars[0]));
         if (mine > 1) bd_issue_page(&tmK, spg[1], kvh, pages_s + BD_PAGE_BYTES, smem_u32(&bars[1]));
     }
+    // the Q fragments of all 16 k-steps stay in registers
+    uint32_t qf[FA_HEAD_DIM / 16][4];
+#pragma unroll
+    for (int ks = 0; ks < FA_HEAD_DIM / 16; ++ks) ldsm_x4(qf[ks], Qs + (lane & 15) * BD_LD + ks * 16 + (lane >> 4) * 8);
     float run_m = -INFINITY, run_s = 0.f;                 // warp g: head g's statistics over the slice
     for (int i = 0; i < mine; ++i) {
         const int j0 = (z + i * Z) * KV_PAGE, cn = min(KV_PAGE, L - j0);
@@ -256,25 +262,27 @@ __global__ void __launch_bounds__(128) bd_att_scores_kernel(const __grid_constan
         // buffer (i + 2) % 3 was read in step i - 1; every warp has passed that step's barrier after its MMAs
         if (tid == 0 && i + 2 < mine) bd_issue_page(&tmK, spg[i + 2], kvh, pages_s + ((i + 2) % BD_NBUF) * BD_PAGE_BYTES, smem_u32(&bars[(i + 2) % BD_NBUF]));
         bd_wait_bar(smem_u32(&bars[i % BD_NBUF]), (uint32_t)((i / BD_NBUF) & 1), status);
-        // warp w: keys [16w, 16w+16) = 2 tiles of 8 keys
-        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        // warp w: keys [16w, 16w+16) = 2 tiles of 8 keys; even and odd k-steps on separate accumulators (two chains of 8)
+        float acc[2][2][4];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) acc[e >> 3][(e >> 2) & 1][e & 3] = 0.f;
         const int krow = warp * 16 + (lane & 7) + 8 * (lane >> 4);
-#pragma unroll 4
+        float (*sp)[BD_CHUNK] = ssc[i & 1];
+#pragma unroll
         for (int ks = 0; ks < FA_HEAD_DIM / 16; ++ks) {
-            uint32_t a[4], bb[4];
-            ldsm_x4(a, Qs + (lane & 15) * BD_LD + ks * 16 + (lane >> 4) * 8);
+            uint32_t bb[4];
             const uint32_t baddr = Kc + bd_page_off(krow, ks * 16 + 8 * ((lane >> 3) & 1));
             asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];" : "=r"(bb[0]), "=r"(bb[1]), "=r"(bb[2]), "=r"(bb[3]) : "r"(baddr));
-            mma_16816(acc[0], a, bb[0], bb[1]);
-            mma_16816(acc[1], a, bb[2], bb[3]);
+            mma_16816(acc[ks & 1][0], qf[ks], bb[0], bb[1]);
+            mma_16816(acc[ks & 1][1], qf[ks], bb[2], bb[3]);
         }
         {   // accumulator rows 0-3 (g = lane/4 < 4) are the four heads; columns 2c, 2c+1 of each 8-key tile
             const int g = lane >> 2, cc = lane & 3;
             if (g < FA_GQA) {
 #pragma unroll
                 for (int nt = 0; nt < 2; ++nt) {
-                    ssc[g][warp * 16 + nt * 8 + 2 * cc] = rbf(acc[nt][0]) * 0.0625f;
-                    ssc[g][warp * 16 + nt * 8 + 2 * cc + 1] = rbf(acc[nt][1]) * 0.0625f;
+                    sp[g][warp * 16 + nt * 8 + 2 * cc] = rbf(acc[0][nt][0] + acc[1][nt][0]) * 0.0625f;
+                    sp[g][warp * 16 + nt * 8 + 2 * cc + 1] = rbf(acc[0][nt][1] + acc[1][nt][1]) * 0.0625f;
                 }
             }
         }
@@ -282,18 +290,18 @@ __global__ void __launch_bounds__(128) bd_att_scores_kernel(const __grid_constan
         {   // warp g: statistics of head g over this page, folded into the slice's; scores to global
             const int g = warp;
             float mx = -INFINITY;
-            for (int j = lane; j < cn; j += 32) mx = fmaxf(mx, ssc[g][j]);
+            for (int j = lane; j < cn; j += 32) mx = fmaxf(mx, sp[g][j]);
             mx = warp_max(mx);
             float sm = 0.f;
-            for (int j = lane; j < cn; j += 32) sm += expf(ssc[g][j] - mx);
+            for (int j = lane; j < cn; j += 32) sm += expf(sp[g][j] - mx);
             sm = warp_sum(sm);
             const float nm = fmaxf(run_m, mx);
             run_s = (run_m == -INFINITY ? 0.f : run_s * expf(run_m - nm)) + sm * expf(mx - nm);
             run_m = nm;
             float* dst = scores + ((size_t)b * FA_Q_HEADS + kvh * FA_GQA + g) * max_ctx + j0;
-            for (int j = lane; j < cn; j += 32) dst[j] = ssc[g][j];
+            for (int j = lane; j < cn; j += 32) dst[j] = sp[g][j];
         }
-        __syncthreads();                                 // ssc is free for the next page
+        // the other score buffer is written next; this one again two pages on, after the next page's barrier
     }
     if (lane == 0) {
         float* st = stats + (((size_t)b * FA_Q_HEADS + kvh * FA_GQA + warp) * max_slices + z) * 2;
@@ -346,17 +354,25 @@ __global__ void __launch_bounds__(128) bd_att_pv_kernel(const __grid_constant__ 
     float acc[8][4];
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) { acc[nt][0] = 0.f; acc[nt][1] = 0.f; acc[nt][2] = 0.f; acc[nt][3] = 0.f; }
+    // a thread forms two P values per page (heads tid / 64 and tid / 64 + 2, position tid % 64); their scores are fetched one
+    // page ahead, so the global-memory latency hides behind the MMAs of the page before
+    const int pj = tid & 63, pg0 = tid >> 6;
+    const float* sc0 = scores + ((size_t)b * FA_Q_HEADS + kvh * FA_GQA + pg0) * max_ctx;
+    const float* sc1 = sc0 + (size_t)2 * max_ctx;
+    float s_next0 = 0.f, s_next1 = 0.f;
+    if (z * KV_PAGE + pj < L) { s_next0 = sc0[z * KV_PAGE + pj]; s_next1 = sc1[z * KV_PAGE + pj]; }
     for (int i = 0; i < mine; ++i) {
         const int j0 = (z + i * Z) * KV_PAGE, cn = min(KV_PAGE, L - j0);
         const uint32_t Vc = pages_s + (i % BD_NBUF) * BD_PAGE_BYTES;
         if (tid == 0 && i + 2 < mine) bd_issue_page(&tmV, spg[i + 2], kvh, pages_s + ((i + 2) % BD_NBUF) * BD_PAGE_BYTES, smem_u32(&bars[(i + 2) % BD_NBUF]));
-        // P of this page while the copies fly: 4 heads x 64 positions, two per thread
-        for (int e = tid; e < FA_GQA * BD_CHUNK; e += 128) {
-            const int g = e / BD_CHUNK, j = e % BD_CHUNK;
-            float pv = 0.f;
-            if (j < cn) pv = rbf(expf(scores[((size_t)b * FA_Q_HEADS + kvh * FA_GQA + g) * max_ctx + j0 + j] - sml[g][0]) / sml[g][1]);
-            Ps[g * BD_PLD + j] = f2bf(pv);
+        const float s_cur0 = s_next0, s_cur1 = s_next1;
+        if (i + 1 < mine) {
+            const int jn = (z + (i + 1) * Z) * KV_PAGE + pj;
+            if (jn < L) { s_next0 = sc0[jn]; s_next1 = sc1[jn]; }
         }
+        // P of this page while the copies fly
+        Ps[pg0 * BD_PLD + pj] = f2bf(pj < cn ? rbf(expf(s_cur0 - sml[pg0][0]) / sml[pg0][1]) : 0.f);
+        Ps[(pg0 + 2) * BD_PLD + pj] = f2bf(pj < cn ? rbf(expf(s_cur1 - sml[pg0 + 2][0]) / sml[pg0 + 2][1]) : 0.f);
         bd_wait_bar(smem_u32(&bars[i % BD_NBUF]), (uint32_t)((i / BD_NBUF) & 1), status);
         if (cn < KV_PAGE) {
             // rows past the sequence's end hold whatever the pool has there; P is zero for them, but 0 x NaN is not: clear them
