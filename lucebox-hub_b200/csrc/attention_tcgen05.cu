@@ -10,8 +10,8 @@
 //   warp 1     one thread issues tcgen05.mma: S[128 x 64] = Q K^T (16 instructions of K = 16), and in pass 2
 //              O[128 x 256] += P V (4 instructions, B = the V^T rows, so every operand is K-major with 128-byte swizzle:
 //              the layout of the GEMM in gemm_tcgen05.cu)
-//   warps 2-5  softmax: thread = row; tcgen05.ld brings the row's 64 scores into registers, so maximum, normaliser and
-//              the P values need no shuffles.  Softmax over the whole row in two passes over the causal key range: pass 1 the
+//   warps 2-9  softmax: two threads per row (32 keys of a chunk each); tcgen05.ld brings the scores into registers, so
+//              maximum, normaliser and the P values need no shuffles.  Softmax over the whole row in two passes over the causal key range: pass 1 the
 //              running row maximum and normaliser; pass 2 recomputes the same scores (same instructions, same values), writes
 //              P = bf16(exp(s - m) / l) as the swizzled A operand of P.V (exp as 2^x on the special-function unit, the
 //              division as a product with 1 / l).  At the end the O row comes from TMEM, is rounded,
@@ -30,7 +30,7 @@ bool make_tmap_bf16(CUtensorMap* tm, const void* ptr, int rank, const unsigned l
                     const unsigned* box);      // gemm_tcgen05.cu
 
 constexpr int AT_Q = 32, AT_ROWS = AT_Q * FA_GQA, AT_KEYS = 64;
-constexpr int AT_THREADS = 192;
+constexpr int AT_THREADS = 320;            // copy warp, MMA warp, eight softmax warps
 constexpr uint32_t AT_Q_BYTES = AT_ROWS * FA_HEAD_DIM * 2;          // 64 KB: four 16 KB blocks of 64 dims
 constexpr uint32_t AT_K_BYTES = AT_KEYS * FA_HEAD_DIM * 2;          // 32 KB: four 8 KB blocks of 64 dims
 constexpr uint32_t AT_V_BYTES = FA_HEAD_DIM * AT_KEYS * 2;          // 32 KB: 256 rows (dims) x 128 bytes (64 keys)
@@ -152,7 +152,7 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_c
         asm volatile("prefetch.tensormap [%0];" ::"l"(&tmK) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(&tmVT) : "memory");
         *s_abort = 0;
-        for (int i = 0; i < 18; ++i) mbar_init(B(i), (i >= 11 && i <= 14) ? 4u : 1u);    // sfree / pfull: one arrival per softmax warp
+        for (int i = 0; i < 18; ++i) mbar_init(B(i), (i >= 11 && i <= 14) ? 8u : 1u);    // sfree / pfull: one arrival per softmax warp
         mbar_fence_init();
     }
     if (warp == 1) {
@@ -229,45 +229,59 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_c
             at_commit(B(17));                // output complete (also fires after an abort so the softmax warps wake)
         }
     } else {
-        // ---- softmax warps: warp w may touch TMEM lanes [32 (w % 4), +32); thread = row ----
-        const int qd = warp & 3, r = qd * 32 + lane;
+        // ---- softmax warps: warp w may touch TMEM lanes [32 (w % 4), +32).  Two threads per row: warps 2-5 take the first 32
+        // keys of a chunk (and the first 128 output dimensions), warps 6-9 the other half, so each sub-partition has two warps
+        // to interleave.  In pass 1 a thread keeps the maximum and normaliser of its own keys; the pair is merged once, through
+        // shared memory, before pass 2. ----
+        const int qd = warp & 3, half = (warp - 2) >> 2, r = qd * 32 + lane;
         const int t = q0 + r / FA_GQA, head = kvh * FA_GQA + r % FA_GQA;
         const uint32_t trow = tmem_base + ((uint32_t)(qd * 32) << 16);
+        const bool live = t < p.S;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
-        for (int item = 0; item < 2 * nchunks; ++item) {
-            const int pass = item >= nchunks, c = pass ? item - nchunks : item, j0 = c * AT_KEYS;
+        float2* ml_x = reinterpret_cast<float2*>(p_ptr);       // [half][row]: the (idle) P tiles carry the exchange after pass 1
+        for (int pass_i = 0; pass_i < 2; ++pass_i) {
+        if (pass_i == 1) {
+            // merge the two halves of every row.  Every softmax thread executes these two barriers exactly once, whatever
+            // happened in pass 1, and no P tile is written before the second one.
+            ml_x[half * AT_ROWS + r] = make_float2(m, l);
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            const float2 other = ml_x[(half ^ 1) * AT_ROWS + r];
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            const float n = fmaxf(m, other.x);
+            l = (m == -INFINITY ? 0.f : l * at_exp2((m - n) * AT_LOG2E)) + (other.x == -INFINITY ? 0.f : other.y * at_exp2((other.x - n) * AT_LOG2E));
+            m = n;
+        }
+        for (int item = pass_i * nchunks; item < (pass_i + 1) * nchunks && ok; ++item) {
+            const int pass = pass_i, c = pass ? item - nchunks : item, j0 = c * AT_KEYS + half * 32;
             const int sb = item & 1;
             ok = __all_sync(0xffffffffu, ok && at_wait(B(9 + sb), (item >> 1) & 1, p.err, s_abort));
             if (!ok) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            uint32_t sv[2][32];
-            at_ld32(trow + AT_TMEM_S + sb * AT_KEYS, sv[0]);
-            at_ld32(trow + AT_TMEM_S + sb * AT_KEYS + 32, sv[1]);
+            uint32_t sv[32];
+            at_ld32(trow + AT_TMEM_S + sb * AT_KEYS + half * 32, sv);
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
-            if (lane == 0) mbar_arrive(B(11 + sb), 1);             // this warp's rows of S are in registers
+            if (lane == 0) mbar_arrive(B(11 + sb), 1);             // this warp's part of S is in registers
             // the chunk needs the causal mask only where it reaches past this row's position (the last chunk or two of a row)
-            const bool live = t < p.S, diag = j0 + AT_KEYS - 1 > t;
+            const bool diag = j0 + 31 > t;
             if (!pass) {
                 float cm = -INFINITY;
 #pragma unroll
-                for (int hf = 0; hf < 2; ++hf)
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        float s = rbf(__uint_as_float(sv[hf][j])) * 0.0625f;
-                        if (diag && j0 + hf * 32 + j > t) s = -INFINITY;
-                        sv[hf][j] = __float_as_uint(s);
-                        cm = fmaxf(cm, s);
-                    }
+                for (int j = 0; j < 32; ++j) {
+                    float sc = rbf(__uint_as_float(sv[j])) * 0.0625f;
+                    if (diag && j0 + j > t) sc = -INFINITY;
+                    sv[j] = __float_as_uint(sc);
+                    cm = fmaxf(cm, sc);
+                }
                 if (live && cm != -INFINITY) {
                     const float n = fmaxf(m, cm), nl = n * AT_LOG2E;
                     float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        s0 += at_exp2(fmaf(__uint_as_float(sv[0][j]), AT_LOG2E, -nl));
-                        s1 += at_exp2(fmaf(__uint_as_float(sv[1][j]), AT_LOG2E, -nl));
+                    for (int j = 0; j < 32; j += 2) {
+                        s0 += at_exp2(fmaf(__uint_as_float(sv[j]), AT_LOG2E, -nl));
+                        s1 += at_exp2(fmaf(__uint_as_float(sv[j + 1]), AT_LOG2E, -nl));
                     }
                     l = (m == -INFINITY ? 0.f : l * at_exp2((m - n) * AT_LOG2E)) + (s0 + s1);
                     m = n;
@@ -277,24 +291,25 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_c
                 if (c >= 2) ok = at_wait(B(15 + pb), ((c >> 1) - 1) & 1, p.err, s_abort);      // P V of two chunks back has read this tile
                 ok = __all_sync(0xffffffffu, ok);
                 if (!ok) break;
-                // P row as 8 pieces of 16 bytes (8 keys each), piece c8 at position c8 ^ (r mod 8) of the row's 128 bytes
+                // this thread's half of the P row: 4 pieces of 16 bytes (8 keys each), piece c8 at position c8 ^ (r mod 8)
                 const float ml = m * AT_LOG2E, inv_l = (live && l > 0.f) ? 1.0f / l : 0.f;
 #pragma unroll
-                for (int c8 = 0; c8 < 8; ++c8) {
+                for (int c4 = 0; c4 < 4; ++c4) {
                     uint32_t w[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         float pv[2];
 #pragma unroll
                         for (int h2 = 0; h2 < 2; ++h2) {
-                            const int jj = c8 * 8 + 2 * e + h2;
-                            const float s = rbf(__uint_as_float(sv[jj >> 5][jj & 31])) * 0.0625f;
-                            pv[h2] = at_exp2(fmaf(s, AT_LOG2E, -ml)) * inv_l;
+                            const int jj = c4 * 8 + 2 * e + h2;
+                            const float sc = rbf(__uint_as_float(sv[jj])) * 0.0625f;
+                            pv[h2] = at_exp2(fmaf(sc, AT_LOG2E, -ml)) * inv_l;
                             if (diag && j0 + jj > t) pv[h2] = 0.f;
                         }
                         const __nv_bfloat162 pr = __floats2bfloat162_rn(pv[0], pv[1]);
                         w[e] = *reinterpret_cast<const uint32_t*>(&pr);
                     }
+                    const int c8 = half * 4 + c4;
                     *reinterpret_cast<uint4*>(p_ptr + pb * AT_P_BYTES + r * 128 + ((c8 ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");      // generic-proxy writes -> visible to the MMA
@@ -302,18 +317,19 @@ attention_tcgen05_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_c
                 if (lane == 0) mbar_arrive(B(13 + pb), 1);
             }
         }
-        // ---- output: bf16(P.V) * bf16(sigmoid(gate)) ----
+        }
+        // ---- output: bf16(P.V) * bf16(sigmoid(gate)); this thread's 128 of the row's 256 dimensions ----
         ok = __all_sync(0xffffffffu, at_wait(B(17), 0, p.err, s_abort) && ok && !*s_abort);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (ok) {
             const bf16* gate = p.proj + (size_t)t * p.ldp + head * 2 * FA_HEAD_DIM + FA_HEAD_DIM;
             bf16* dst = p.out + (size_t)t * FA_Q_SIZE + head * FA_HEAD_DIM;
 #pragma unroll 1
-            for (int cb = 0; cb < FA_HEAD_DIM / 32; ++cb) {
+            for (int cb = half * 4; cb < half * 4 + 4; ++cb) {
                 uint32_t ov[32];
                 at_ld32(trow + (uint32_t)(cb * 32), ov);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (t < p.S) {
+                if (live) {
 #pragma unroll
                     for (int j = 0; j < 32; j += 8) {
                         const uint4 gr = *reinterpret_cast<const uint4*>(gate + cb * 32 + j);

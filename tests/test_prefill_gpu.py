@@ -175,6 +175,47 @@ def test_prefill_sweep_sizes_teacher_forced(full_weights_cpu, S):
         assert float((got_c != ref_c).float().mean()) < 0.05
 
 
+@pytest.mark.parametrize("S", [1, 2, 31, 33, 63, 64, 65, 127, 129, 257])
+def test_prefill_ragged_lengths_teacher_forced(ctx, S):
+    """Prompt lengths around the tile edges of the attention kernel (32-query blocks, 64-key chunks, a V^T scratch padded to
+    64 positions) and of the chunk-64 delta rule, all 24 layers teacher forced: the last position's output of every layer,
+    the K / V rows of the attention layers and the DeltaNet states."""
+    D, dec = ctx["D"], ctx["dec"]
+    from qwen35_b200.weights import make_token_ids
+    ids = make_token_ids(S, 1000 + S, D.vocab)
+    o = ctx["Oracle"](ctx["w"], D, 1024)
+    o.keep_all = True
+    o.prefill(ids)
+    teacher = torch.zeros(24, S, 1024, dtype=torch.bfloat16)
+    for l in range(1, 24):
+        teacher[l] = o.trace_all[l - 1]
+    dbg = torch.zeros(24, 1024, dtype=torch.bfloat16, device="cuda")
+    logits = torch.zeros(D.vocab, device="cuda")
+    dec.prefill_tokens(ids.cuda(), logits_out=logits, dbg_teacher=teacher.cuda(), dbg_hidden=dbg)
+    dec.check_status()
+    trace, got = torch.stack(o.trace), dbg.cpu()
+    att = [l for l in range(24) if D.layer_types[l] == 1]
+    max_abs = float((got.float() - trace.float()).abs().max())
+    att_abs = float((got[att].float() - trace[att].float()).abs().max())
+    frac = float((got != trace).float().mean())
+    print(f"prefill S={S} teacher forced: {frac:.3%} of last-position elements differ, max abs {max_abs} (attention layers {att_abs})")
+    assert max_abs <= LAYER_ABS_TOL and frac < 0.18
+    k_ref, v_ref = torch.stack(o.k_cache), torch.stack(o.v_cache)
+    for got_c, ref_c in ((dec._fa_k_cache[:, :, :S].cpu(), k_ref), (dec._fa_v_cache[:, :, :S].cpu(), v_ref)):
+        d = (got_c.float() - ref_c.float()).abs()
+        assert float((d / (ref_c.float().abs() * 2.0 ** -8 + 2.0 ** -9)).max()) <= 8.0
+    # DeltaNet states.  With few tokens in the state one flipped bf16 rounding of a head's L2-norm scale (the f32 sum of squares
+    # lands on the other side of a rounding boundary in a different summation order) shows through undiluted: that head's
+    # keys move by one bf16 last place, its state by 2^-8 .. 2^-7 relative, every other head stays at ~1e-7 (measured: one
+    # such head in one layer at S = 31, 192, 257).  So: every head within 2^-6, and all but a few layers within the 1e-3 that
+    # whole layers meet at 512 tokens and more.
+    st, sr = dec._dn_states.cpu(), o.dn_states_ref_layout()
+    head_rel = ((st - sr).flatten(2).norm(dim=2) / sr.flatten(2).norm(dim=2).clamp_min(1e-30))
+    layer_rel = [float((st[i] - sr[i]).norm() / sr[i].norm()) for i in range(18)]
+    assert float(head_rel.max()) <= 2.0 ** -6
+    assert sum(r <= STATE_REL_TOL for r in layer_rel) >= 15
+
+
 def test_prefill_mega_form_equals_fused_form(ctx):
     """The prompt pass without the fused-weight table (what launch_prefill_bf16_mega runs: one GEMM per matrix of the
     layer record, SiLU * up as its own kernel) against the fused pass: same matrices, same roundings.  Only the split-K
