@@ -396,7 +396,7 @@ def run_ours(args):
                          "algorithmic_bytes_per_launch": alg_bytes, "launch_ms": kern_avg},
             "e2e": {"value": world * GEN * e2e_steps / (e2e_ms * 1e-3), "unit": "tok/s",
                     "h2d_bytes_per_step": GEN * 4, "d2h_bytes_per_step": GEN * 4,
-                    "path": "Decoder.step(): one launch_decode + one 4-byte device->host read per token"},
+                    "path": "Decoder.step(): per token one launch_decode (the token id travels as a launch argument), the next token stored by the kernel into pinned host memory and read after a stream synchronisation"},
             "gpu_launches": launches, "clocks": clocks,
         }
         if parity is not None:

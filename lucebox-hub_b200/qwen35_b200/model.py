@@ -283,6 +283,11 @@ class Decoder:
         self._conv_bufs = torch.zeros(n_dn, DN_CONV_CHANNELS, DN_CONV_KERNEL, dtype=torch.float32, device=dev)
         self._hidden = torch.empty(HIDDEN_SIZE, dtype=torch.bfloat16, device=dev)
         self._out_token = torch.zeros(1, dtype=torch.int32, device=dev)
+        # step(): the kernel stores the token straight into pinned host memory (same address on the device under unified
+        # addressing), so reading it back costs a stream synchronisation and no copy call; the argument tuple is built once
+        self._out_token_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self._out_token_view = self._out_token_host.numpy()
+        self._step_args = None
         self._token_buf = torch.zeros(1, dtype=torch.int32, device=dev)
 
     # ---- helpers ---------------------------------------------------------------------------
@@ -328,18 +333,24 @@ class Decoder:
             self._run(self._args(token_imm=int(token_id), n_steps=1))
             self._position += 1
             return int(self._out_token.item())
-        with torch.cuda.device(self.device):
+        if self._step_args is None:
             none = None
-            _capi.check(self._lib.launch_decode(
-                int(token_id), self._out_token.data_ptr(),
-                self._embed_weight.data_ptr(), self._layer_weights_packed.data_ptr(),
-                self._final_norm_weight.data_ptr(), self._lm_head_weight.data_ptr(),
-                self._fa_k_cache.data_ptr(), self._fa_v_cache.data_ptr(),
-                self._dn_states.data_ptr(), self._conv_bufs.data_ptr(),
-                self._hidden.data_ptr(), *([none] * 10), *([none] * 5),
-                self._position, self.max_seq_len, self._stream()), "launch_decode")
+            self._step_args = (self._out_token_host.data_ptr(),
+                               self._embed_weight.data_ptr(), self._layer_weights_packed.data_ptr(),
+                               self._final_norm_weight.data_ptr(), self._lm_head_weight.data_ptr(),
+                               self._fa_k_cache.data_ptr(), self._fa_v_cache.data_ptr(),
+                               self._dn_states.data_ptr(), self._conv_bufs.data_ptr(),
+                               self._hidden.data_ptr(), *([none] * 10), *([none] * 5))
+            self._step_dev = torch.device(self.device)
+            self._step_dev_index = self._step_dev.index if self._step_dev.index is not None else torch.cuda.current_device()
+        if torch.cuda.current_device() != self._step_dev_index:
+            torch.cuda.set_device(self._step_dev_index)
+        stream = torch.cuda.current_stream(self._step_dev)
+        _capi.check(self._lib.launch_decode(int(token_id), *self._step_args, self._position, self.max_seq_len,
+                                            C.c_void_p(stream.cuda_stream)), "launch_decode")
         self._position += 1
-        return int(self._out_token.item())
+        stream.synchronize()
+        return int(self._out_token_view[0])
 
     def step_many(self, token_id: int, num_steps: int, logits_out=None, dbg_time=None, dbg_time_cta=0) -> torch.Tensor:
         """`num_steps` greedy steps in one launch, tokens fed back on the device
