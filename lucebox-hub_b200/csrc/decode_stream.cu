@@ -688,6 +688,14 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                     const bool att_cta = ag.att_cta;
                     att_owner = ag.owns_pos;
                     if (att_cta) {
+                        // this warp's first two key rows do not depend on the current token: request them before the q / k / v of
+                        // the token are awaited, so their L2 latency runs under the hand-off
+                        uint4 k_pre_a = make_uint4(0, 0, 0, 0), k_pre_b = k_pre_a;
+                        {
+                            const int j = j0 + warp, jb = j + NCONS_WARPS;
+                            if (j < j1 && j != pos) k_pre_a = ld_cg(reinterpret_cast<const uint4*>(kc + ((size_t)kvh * a.max_seq_len + j) * FA_HEAD_DIM) + lane);
+                            if (jb < j1 && jb != pos) k_pre_b = ld_cg(reinterpret_cast<const uint4*>(kc + ((size_t)kvh * a.max_seq_len + jb) * FA_HEAD_DIM) + lane);
+                        }
                         if (warp < FA_GQA + 1) {
                             // warps 0..3: the four query heads of this kv head; warp 4: the new key.
                             // lane l holds elements {2l, 2l+1} + 64*i, i = 0..3 (four flagged words)
@@ -745,9 +753,12 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                                 for (int i = 0; i < 8; ++i) qr[g][i] = s.q[g][lane * 8 + i];
                             for (int j = j0 + warp; j < j1; j += 2 * NCONS_WARPS) {
                                 const int jb = j + NCONS_WARPS;
-                                uint4 ka = make_uint4(0, 0, 0, 0), kb = ka;
-                                if (j != pos) ka = ld_cg(reinterpret_cast<const uint4*>(kc + ((size_t)kvh * a.max_seq_len + j) * FA_HEAD_DIM) + lane);
-                                if (jb < j1 && jb != pos) kb = ld_cg(reinterpret_cast<const uint4*>(kc + ((size_t)kvh * a.max_seq_len + jb) * FA_HEAD_DIM) + lane);
+                                uint4 ka = k_pre_a, kb = k_pre_b;
+                                if (j != j0 + warp) {          // later rounds of a long chunk
+                                    ka = make_uint4(0, 0, 0, 0); kb = ka;
+                                    if (j != pos) ka = ld_cg(reinterpret_cast<const uint4*>(kc + ((size_t)kvh * a.max_seq_len + j) * FA_HEAD_DIM) + lane);
+                                    if (jb < j1 && jb != pos) kb = ld_cg(reinterpret_cast<const uint4*>(kc + ((size_t)kvh * a.max_seq_len + jb) * FA_HEAD_DIM) + lane);
+                                }
 #pragma unroll
                                 for (int r = 0; r < 2; ++r) {
                                     const int jj = r ? jb : j;
