@@ -266,6 +266,7 @@ struct ChunkScratch {          // one record per (head, chunk), floats; every ar
 static_assert(sizeof(ChunkScratch) % 16 == 0, "records must keep 16-byte alignment");
 
 constexpr int CL_THREADS = 512;
+constexpr float CL_QSCALE = 0.08838834764831845f;        // 1 / sqrt(128)
 constexpr int CL_LD = DN_K + 4;                          // q, k: A operands (row-major) and, for k, the transposed B operand: bank = 4 g + t
 constexpr int CL_LDB = DN_K + 8;                         // v beta, k beta exp(gc): B operands [token][dim]: bank = 8 t + g
 constexpr int CL_LDA = DN_CHUNK + 4;                     // T: A operand of the last two products
@@ -305,9 +306,10 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
             kr = *reinterpret_cast<const uint4*>(row + DN_QK_SIZE);
             vr = *reinterpret_cast<const uint4*>(row + 2 * DN_QK_SIZE);
         }
-        const float qs_ = 0.08838834764831845f;
-        *reinterpret_cast<float4*>(sq + i * CL_LD + d) = make_float4(bf_lo(qr.x) * qs_, bf_hi(qr.x) * qs_, bf_lo(qr.y) * qs_, bf_hi(qr.y) * qs_);
-        *reinterpret_cast<float4*>(sq + i * CL_LD + d + 4) = make_float4(bf_lo(qr.z) * qs_, bf_hi(qr.z) * qs_, bf_lo(qr.w) * qs_, bf_hi(qr.w) * qs_);
+        // q and k stay the bf16 values they are (8 significant bits: exact as tf32 operands); the 1 / sqrt(128) of q is applied to
+        // the products below
+        *reinterpret_cast<float4*>(sq + i * CL_LD + d) = make_float4(bf_lo(qr.x), bf_hi(qr.x), bf_lo(qr.y), bf_hi(qr.y));
+        *reinterpret_cast<float4*>(sq + i * CL_LD + d + 4) = make_float4(bf_lo(qr.z), bf_hi(qr.z), bf_lo(qr.w), bf_hi(qr.w));
         *reinterpret_cast<float4*>(sk + i * CL_LD + d) = make_float4(bf_lo(kr.x), bf_hi(kr.x), bf_lo(kr.y), bf_hi(kr.y));
         *reinterpret_cast<float4*>(sk + i * CL_LD + d + 4) = make_float4(bf_lo(kr.z), bf_hi(kr.z), bf_lo(kr.w), bf_hi(kr.w));
         *reinterpret_cast<float4*>(sv + i * CL_LDB + d) = make_float4(bf_lo(vr.x), bf_hi(vr.x), bf_lo(vr.y), bf_hi(vr.y));
@@ -328,7 +330,7 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
             const float4 kv = *reinterpret_cast<const float4*>(sk + i * CL_LD + d), qv = *reinterpret_cast<const float4*>(sq + i * CL_LD + d);
             float4 vv = *reinterpret_cast<const float4*>(sv + i * CL_LDB + d);
             const float ei = se[i], kd = expf(g_last - sg[i]), bi = sb[i];
-            *reinterpret_cast<float4*>(&out.qs[i][d]) = make_float4(qv.x * ei, qv.y * ei, qv.z * ei, qv.w * ei);
+            *reinterpret_cast<float4*>(&out.qs[i][d]) = make_float4((qv.x * CL_QSCALE) * ei, (qv.y * CL_QSCALE) * ei, (qv.z * CL_QSCALE) * ei, (qv.w * CL_QSCALE) * ei);
             *reinterpret_cast<float4*>(&out.ks[i][d]) = make_float4(kv.x * kd, kv.y * kd, kv.z * kd, kv.w * kd);
             vv.x *= bi; vv.y *= bi; vv.z *= bi; vv.w *= bi;
             *reinterpret_cast<float4*>(sv + i * CL_LDB + d) = vv;
@@ -345,30 +347,31 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
         const int ntn = (u == 2 || u >= 5) ? 2 : 3;
         const bool is_q = warp >= 8;
         const float* A = is_q ? sq : sk;
-        float acc3[3][3][4];
+        // Both operands are bf16 values, exact in tf32: one MMA per tile and k-step, no hi / lo split (the f32 products of the
+        // chunk-64 formulation, summed on the tensor cores).  Two halves of the k range on separate accumulators.
+        float acc2[2][3][4];
 #pragma unroll
-        for (int n = 0; n < 3; ++n)
-#pragma unroll
-            for (int r = 0; r < 12; ++r) acc3[n][r >> 2][r & 3] = 0.f;
+        for (int e = 0; e < 24; ++e) acc2[e / 12][(e >> 2) % 3][e & 3] = 0.f;
 #pragma unroll 2
-        for (int k0 = 0; k0 < DN_K; k0 += 8) {
-            uint32_t ah[4], al[4];
-            load_a_split(A, CL_LD, mt * 16, k0, ah, al);
+        for (int k0 = 0; k0 < DN_K / 2; k0 += 8) {
 #pragma unroll
-            for (int n = 0; n < 3; ++n)
-                if (n < ntn) {
-                    const float* br = sk + ((nt0 + n) * 8 + gq) * CL_LD + k0 + t4;        // B(k, n) = k[token n][dim k]
-                    uint32_t bh0, bl0, bh1, bl1;
-                    tf32_split(br[0], bh0, bl0);
-                    tf32_split(br[4], bh1, bl1);
-                    mma_3xtf32_terms(acc3[n], ah, al, bh0, bh1, bl0, bl1);
-                }
+            for (int hf = 0; hf < 2; ++hf) {
+                const int kk = k0 + hf * (DN_K / 2);
+                const float* ar = A + (mt * 16 + gq) * CL_LD + kk + t4;
+                const uint32_t af[4] = {__float_as_uint(ar[0]), __float_as_uint(ar[8 * CL_LD]), __float_as_uint(ar[4]), __float_as_uint(ar[8 * CL_LD + 4])};
+#pragma unroll
+                for (int n = 0; n < 3; ++n)
+                    if (n < ntn) {
+                        const float* br = sk + ((nt0 + n) * 8 + gq) * CL_LD + kk + t4;        // B(k, n) = k[token n][dim k]
+                        mma_tf32(acc2[hf][n], af, __float_as_uint(br[0]), __float_as_uint(br[4]));
+                    }
+            }
         }
         float acc[3][4];
 #pragma unroll
         for (int n = 0; n < 3; ++n)
 #pragma unroll
-            for (int r = 0; r < 4; ++r) acc[n][r] = sum_terms(acc3[n], r);
+            for (int r = 0; r < 4; ++r) acc[n][r] = acc2[0][n][r] + acc2[1][n][r];
         // A[i][j] = -(beta_i k_i . k_j) * exp(gc_i - gc_j) for j < i, else 0;   aqk[i][j] = (q_i . k_j) * exp(gc_i - gc_j) for j <= i
 #pragma unroll
         for (int n = 0; n < 3; ++n)
@@ -377,7 +380,7 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
                 for (int r = 0; r < 4; ++r) {
                     const int i = mt * 16 + gq + 8 * (r >> 1), j = (nt0 + n) * 8 + 2 * t4 + (r & 1);
                     const float dec = (j <= i) ? expf(sg[i] - sg[j]) : 0.f;
-                    if (is_q) out.aqk[i][j] = (j <= i) ? acc[n][r] * dec : 0.f;
+                    if (is_q) out.aqk[i][j] = (j <= i) ? (acc[n][r] * CL_QSCALE) * dec : 0.f;
                     else sa[i * CL_LDA + j] = (j < i) ? -((acc[n][r] * sb[i]) * dec) : 0.f;
                 }
         // the tiles above the diagonal blocks were not computed: aqk and A are zero there (the forward substitution reads
