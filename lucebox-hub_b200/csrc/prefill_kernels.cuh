@@ -246,7 +246,8 @@ __device__ __forceinline__ void load_at_split(const float* M, int ld, int m0, in
 // ---- chunk-local part of the gated delta rule: one CTA (16 warps) per (chunk, head) --------------
 // Per chunk of 64 tokens (zero padded): gc = cumsum(g); T = (I + tril((k beta) k^T * decay, -1))^-1 (a unit lower triangular
 // solve); vprime = T (v beta); kcd = T (k beta exp(gc)); aqk = tril(q k^T * decay).  f32 throughout; the four matrix products
-// (k k^T, q k^T, T v, T k) are 3xTF32 tensor-core tiles; the triangular solve runs on the CUDA cores in 16 x 16 blocks.
+// (k k^T, q k^T, T v, T k) run on the tensor cores with q, k, v as exact tf32 operands (they are bf16 values) and only T split
+// hi + lo; the triangular solve runs on the CUDA cores in 16 x 16 blocks.
 // The record the scan kernel reads.  Its arrays have the row pitches of the scan's shared-memory operands (padded against
 // bank conflicts) and vprime is stored by 16-column slice, so that each operand of a scan CTA is ONE contiguous block
 // and moves with a single bulk copy; the pad columns are never read by an mma.
@@ -279,8 +280,8 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
     extern __shared__ __align__(16) float sm[];
     float* sq = sm;                                  // [64][CL_LD]   q / sqrt(128)
     float* sk = sq + DN_CHUNK * CL_LD;               // [64][CL_LD]   k
-    float* sv = sk + DN_CHUNK * CL_LD;               // [64][CL_LDB]  v * beta
-    float* skb = sv + DN_CHUNK * CL_LDB;             // [64][CL_LDB]  k * beta * exp(gc)
+    float* sv = sk + DN_CHUNK * CL_LD;               // [64][CL_LDB]  v
+    float* skb = sv + DN_CHUNK * CL_LDB;             // [64][CL_LDB]  k again, in the B-operand pitch
     float* sa = skb + DN_CHUNK * CL_LDB;             // [64][CL_LDA]  N = -(k beta) k^T * decay, strictly lower
     float* sx = sa + DN_CHUNK * CL_LDA;              // [64][CL_LDA]  T = (I - N)^-1
     float* sw = sx + DN_CHUNK * CL_LDA;              // [3][16][16]   block products of the inversion
@@ -323,18 +324,15 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
     __syncthreads();
     if (tid < DN_CHUNK) { se[tid] = expf(sg[tid]); out.gc[tid] = sg[tid]; }
     __syncthreads();
-    {   // operands of the scan that depend on this chunk only; v * beta and k * beta * exp(gc) for the products below
+    {   // operands of the scan that depend on this chunk only; a copy of k in the B-operand pitch for the products below
         const float g_last = sg[DN_CHUNK - 1];
         for (int e = tid; e < DN_CHUNK * (DN_K / 4); e += CL_THREADS) {
             const int i = e >> 5, d = (e & 31) * 4;
             const float4 kv = *reinterpret_cast<const float4*>(sk + i * CL_LD + d), qv = *reinterpret_cast<const float4*>(sq + i * CL_LD + d);
-            float4 vv = *reinterpret_cast<const float4*>(sv + i * CL_LDB + d);
-            const float ei = se[i], kd = expf(g_last - sg[i]), bi = sb[i];
+            const float ei = se[i], kd = expf(g_last - sg[i]);
             *reinterpret_cast<float4*>(&out.qs[i][d]) = make_float4((qv.x * CL_QSCALE) * ei, (qv.y * CL_QSCALE) * ei, (qv.z * CL_QSCALE) * ei, (qv.w * CL_QSCALE) * ei);
             *reinterpret_cast<float4*>(&out.ks[i][d]) = make_float4(kv.x * kd, kv.y * kd, kv.z * kd, kv.w * kd);
-            vv.x *= bi; vv.y *= bi; vv.z *= bi; vv.w *= bi;
-            *reinterpret_cast<float4*>(sv + i * CL_LDB + d) = vv;
-            *reinterpret_cast<float4*>(skb + i * CL_LDB + d) = make_float4((kv.x * bi) * ei, (kv.y * bi) * ei, (kv.z * bi) * ei, (kv.w * bi) * ei);
+            *reinterpret_cast<float4*>(skb + i * CL_LDB + d) = kv;
         }
         if (tid == 0) out.eg_last[0] = expf(g_last);
     }
@@ -459,37 +457,42 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
         }
         __syncthreads();
     }
-    // ---- vprime = T (v beta) (warps 0-7), kcd = T (k beta exp(gc)) (warps 8-15): 64 x 128 x 64 with T lower triangular.  A warp
-    // takes a quarter of the 128 columns and two row tiles whose k ranges add up to the same length: (0, 3) or (1, 2).
+    // ---- vprime = T (v beta) (warps 0-7), kcd = T (k beta exp(gc)) (warps 8-15): 64 x 128 x 64 with T lower triangular.
+    // beta_j and beta_j exp(gc_j) belong to the summation index j, so they go into the left operand: T diag(beta) times the
+    // rows of v, T diag(beta exp(gc)) times the rows of k.  v and k are bf16 values, exact as tf32 operands, so only the
+    // left operand is split: two MMAs per tile and k-step instead of three, and no split of the right operand.
+    for (int e = tid; e < DN_CHUNK * DN_CHUNK; e += CL_THREADS) {
+        const int i = e >> 6, j = e & 63;
+        const float tij = (j >> 4) <= (i >> 4) ? sx[i * CL_LDA + j] : 0.f;
+        sa[i * CL_LDA + j] = tij * sb[j];                  // N is no longer needed: its buffer holds T diag(beta)
+        sx[i * CL_LDA + j] = tij * (sb[j] * se[j]);
+    }
+    __syncthreads();
+    // A warp takes a quarter of the 128 columns and two row tiles whose k ranges add up to the same length: (0, 3) or (1, 2).
     {
         const int u = warp & 7, nq = u & 3;
-        const float* Bm = (warp < 8) ? sv : skb;
         const bool to_vp = warp < 8;
+        const float* Bm = to_vp ? sv : skb;
+        const float* Am = to_vp ? sa : sx;
 #pragma unroll
         for (int pass = 0; pass < 2; ++pass) {
             const int mt = (u < 4) ? (pass ? 3 : 0) : (pass ? 2 : 1);
-            float acc3[4][3][4];
+            float acc2[4][2][4];
 #pragma unroll
             for (int n = 0; n < 4; ++n)
 #pragma unroll
-                for (int r = 0; r < 12; ++r) acc3[n][r >> 2][r & 3] = 0.f;
+                for (int r = 0; r < 8; ++r) acc2[n][r >> 2][r & 3] = 0.f;
             for (int k0 = 0; k0 < 16 * (mt + 1); k0 += 8) {
                 uint32_t ah[4], al[4];
-                load_a_split(sx, CL_LDA, mt * 16, k0, ah, al);
+                load_a_split(Am, CL_LDA, mt * 16, k0, ah, al);
 #pragma unroll
                 for (int n = 0; n < 4; ++n) {
                     const float* br = Bm + (k0 + t4) * CL_LDB + nq * 32 + n * 8 + gq;       // B(k, n) = Bm[token k][dim n]
-                    uint32_t bh0, bl0, bh1, bl1;
-                    tf32_split(br[0], bh0, bl0);
-                    tf32_split(br[4 * CL_LDB], bh1, bl1);
-                    mma_3xtf32_terms(acc3[n], ah, al, bh0, bh1, bl0, bl1);
+                    const uint32_t b0 = __float_as_uint(br[0]), b1 = __float_as_uint(br[4 * CL_LDB]);
+                    mma_tf32(acc2[n][0], al, b0, b1);
+                    mma_tf32(acc2[n][1], ah, b0, b1);
                 }
             }
-            float acc[4][4];
-#pragma unroll
-            for (int n = 0; n < 4; ++n)
-#pragma unroll
-                for (int r = 0; r < 4; ++r) acc[n][r] = sum_terms(acc3[n], r);
 #pragma unroll
             for (int n = 0; n < 4; ++n)
 #pragma unroll
@@ -497,7 +500,7 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
                 {
                     const int i = mt * 16 + gq + 8 * hr, d = nq * 32 + n * 8 + 2 * t4;
                     float* dst = to_vp ? &out.vprime[d / SCAN_VW][i][d % SCAN_VW] : &out.kcd[i][d];
-                    *reinterpret_cast<float2*>(dst) = make_float2(acc[n][2 * hr], acc[n][2 * hr + 1]);
+                    *reinterpret_cast<float2*>(dst) = make_float2(acc2[n][0][2 * hr] + acc2[n][1][2 * hr], acc2[n][0][2 * hr + 1] + acc2[n][1][2 * hr + 1]);
                 }
         }
     }
