@@ -234,13 +234,13 @@ __device__ __forceinline__ void load_a_split(const float* A, int ld, int m0, int
     tf32_split(A[(m0 + g) * ld + k0 + t + 4], ah[2], al[2]);
     tf32_split(A[(m0 + g + 8) * ld + k0 + t + 4], ah[3], al[3]);
 }
-// the same for A = M^T with M row-major [k][m] (element (m, k) at M[k * ld + m])
-__device__ __forceinline__ void load_at_split(const float* M, int ld, int m0, int k0, uint32_t (&ah)[4], uint32_t (&al)[4]) {
+// A = M^T with M holding values that are exact in tf32 (bf16 inputs): the bits go to the mma as they are
+__device__ __forceinline__ void load_at_exact(const float* M, int ld, int m0, int k0, uint32_t (&a)[4]) {
     const int g = (threadIdx.x & 31) >> 2, t = threadIdx.x & 3;
-    tf32_split(M[(k0 + t) * ld + m0 + g], ah[0], al[0]);
-    tf32_split(M[(k0 + t) * ld + m0 + g + 8], ah[1], al[1]);
-    tf32_split(M[(k0 + t + 4) * ld + m0 + g], ah[2], al[2]);
-    tf32_split(M[(k0 + t + 4) * ld + m0 + g + 8], ah[3], al[3]);
+    a[0] = __float_as_uint(M[(k0 + t) * ld + m0 + g]);
+    a[1] = __float_as_uint(M[(k0 + t) * ld + m0 + g + 8]);
+    a[2] = __float_as_uint(M[(k0 + t + 4) * ld + m0 + g]);
+    a[3] = __float_as_uint(M[(k0 + t + 4) * ld + m0 + g + 8]);
 }
 
 // ---- chunk-local part of the gated delta rule: one CTA (16 warps) per (chunk, head) --------------
@@ -259,9 +259,9 @@ struct ChunkScratch {          // one record per (head, chunk), floats; every ar
     float vprime[DN_V / SCAN_VW][DN_CHUNK][SCAN_VW];
     float kcd[DN_CHUNK][SCAN_LDA];
     float qs[DN_CHUNK][SCAN_LDA];      // q / sqrt(128) * exp(gc_i): the scan's left operand of q S
-    float ks[DN_CHUNK][SCAN_LDT];      // k * exp(gc_last - gc_i):   the scan's left operand of the state update
+    float ks[DN_CHUNK][SCAN_LDT];      // k as read (bf16 values):   the scan's left operand of the state update, exact in tf32
     float aqk[DN_CHUNK][SCAN_LDQ];
-    float gc[DN_CHUNK];
+    float kdec[DN_CHUNK];              // exp(gc_last - gc_i): the scan scales row i of v_new by it for the state update (follows aqk: one copy)
     float eg_last[4];              // [0] = exp(gc_last)
 };
 static_assert(sizeof(ChunkScratch) % 16 == 0, "records must keep 16-byte alignment");
@@ -322,16 +322,16 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
         for (int i = 0; i < DN_CHUNK; ++i) { acc += sg[i]; sg[i] = acc; }
     }
     __syncthreads();
-    if (tid < DN_CHUNK) { se[tid] = expf(sg[tid]); out.gc[tid] = sg[tid]; }
+    if (tid < DN_CHUNK) { se[tid] = expf(sg[tid]); out.kdec[tid] = expf(sg[DN_CHUNK - 1] - sg[tid]); }
     __syncthreads();
     {   // operands of the scan that depend on this chunk only; a copy of k in the B-operand pitch for the products below
         const float g_last = sg[DN_CHUNK - 1];
         for (int e = tid; e < DN_CHUNK * (DN_K / 4); e += CL_THREADS) {
             const int i = e >> 5, d = (e & 31) * 4;
             const float4 kv = *reinterpret_cast<const float4*>(sk + i * CL_LD + d), qv = *reinterpret_cast<const float4*>(sq + i * CL_LD + d);
-            const float ei = se[i], kd = expf(g_last - sg[i]);
+            const float ei = se[i];
             *reinterpret_cast<float4*>(&out.qs[i][d]) = make_float4((qv.x * CL_QSCALE) * ei, (qv.y * CL_QSCALE) * ei, (qv.z * CL_QSCALE) * ei, (qv.w * CL_QSCALE) * ei);
-            *reinterpret_cast<float4*>(&out.ks[i][d]) = make_float4(kv.x * kd, kv.y * kd, kv.z * kd, kv.w * kd);
+            *reinterpret_cast<float4*>(&out.ks[i][d]) = kv;
             *reinterpret_cast<float4*>(skb + i * CL_LDB + d) = kv;
         }
         if (tid == 0) out.eg_last[0] = expf(g_last);
@@ -508,11 +508,12 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
 
 // ---- scan over chunks: one CTA (8 warps) per (head, 16-wide slice of the value dimension) --------
 // Sequential over the chunks of a head; per chunk  v_new = vprime - kcd S,  out = qs S + aqk v_new,
-// S <- S exp(gc_last) + ks^T v_new  (S = state slice [128 k][16 v]).  All four products run on the tensor cores as
-// 3xTF32 mma.sync tiles:
+// S <- S exp(gc_last) + k^T (e v_new)  (S = state slice [128 k][16 v]).  All four products run on the tensor cores as
+// 3xTF32 mma.sync tiles (two terms where the left operand is exact):
 //   P1  warps 0-3: VP = kcd S, warps 4-7: IT = qs S      (64 x 128 x 16, one 16-row tile and both 8-column tiles per warp)
 //   P2  warps 4-7: out = IT + aqk v_new                   (64 x 64 x 16, lower-triangular: zero k-steps skipped)
-//   P3  all warps: S' = S exp(gc_last) + ks^T v_new       (128 x 64 x 16, one 16-row tile per warp)
+//   P3  all warps: S' = S exp(gc_last) + k^T (e v_new)    (128 x 64 x 16, one 16-row tile per warp; e_i = exp(gc_last - gc_i);
+//                                                          k is exact in tf32: two mma per tile instead of three)
 // The state slice lives in registers as the f32 accumulator fragment of P3 from chunk to chunk (no precision is lost to
 // the operand split); shared memory holds its hi / lo split as the B operand of the next chunk's P1, and v_new likewise.
 // The left operands are plain copies of what the chunk-local kernel wrote, in the layout it wrote them.  A ninth warp brings
@@ -521,9 +522,9 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
 constexpr int SCAN_CONS = 256;              // compute threads
 constexpr int SCAN_THREADS = SCAN_CONS + 32;
 constexpr int SCAN_LDB = SCAN_VW + 8;       // B operands (state and v_new, hi and lo): bank = 24 t + g
-constexpr int CHUNK_SCAN_SMEM = (2 * DN_CHUNK * SCAN_LDA + DN_CHUNK * SCAN_LDT + DN_CHUNK * SCAN_LDQ + DN_CHUNK * SCAN_VW +
-                                 2 * DN_K * SCAN_LDB + 2 * DN_CHUNK * SCAN_LDB) * 4 + 64;
-constexpr uint32_t SCAN_G1_BYTES = DN_CHUNK * (2 * SCAN_LDA + SCAN_VW) * 4, SCAN_G2_BYTES = DN_CHUNK * (SCAN_LDT + SCAN_LDQ) * 4;
+constexpr int CHUNK_SCAN_SMEM = (2 * DN_CHUNK * SCAN_LDA + DN_CHUNK * SCAN_LDT + DN_CHUNK * SCAN_LDQ + DN_CHUNK + DN_CHUNK * SCAN_VW +
+                                 2 * DN_K * SCAN_LDB + 4 * DN_CHUNK * SCAN_LDB) * 4 + 64;
+constexpr uint32_t SCAN_G1_BYTES = DN_CHUNK * (2 * SCAN_LDA + SCAN_VW) * 4, SCAN_G2_BYTES = DN_CHUNK * (SCAN_LDT + SCAN_LDQ + 1) * 4;
 constexpr unsigned SCAN_WAIT_LIMIT = 1u << 26;      // a bounded wait: a copy that never lands ends the loop instead of hanging
 
 __device__ __forceinline__ void scan_wait(uint32_t bar, uint32_t parity, int* err) {
@@ -541,12 +542,15 @@ static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(c
     float* sq = skcd + DN_CHUNK * SCAN_LDA;             // [64][SCAN_LDA]
     float* sk = sq + DN_CHUNK * SCAN_LDA;               // [64][SCAN_LDT]
     float* sa = sk + DN_CHUNK * SCAN_LDT;               // [64][SCAN_LDQ]
-    float* svp = sa + DN_CHUNK * SCAN_LDQ;              // [64][16]
+    float* skd = sa + DN_CHUNK * SCAN_LDQ;              // [64] exp(gc_last - gc_i), lands with aqk
+    float* svp = skd + DN_CHUNK;                        // [64][16]
     uint32_t* sth = reinterpret_cast<uint32_t*>(svp + DN_CHUNK * SCAN_VW);   // [128][SCAN_LDB] state, tf32 hi
     uint32_t* stl = sth + DN_K * SCAN_LDB;                                   //                  state, tf32 lo
     uint32_t* vnh = stl + DN_K * SCAN_LDB;                                   // [64][SCAN_LDB]  v_new, tf32 hi
     uint32_t* vnl = vnh + DN_CHUNK * SCAN_LDB;                               //                  v_new, tf32 lo
-    u64* bars = reinterpret_cast<u64*>(vnl + DN_CHUNK * SCAN_LDB);           // full1, full2, empty1, empty2
+    uint32_t* vkh = vnl + DN_CHUNK * SCAN_LDB;                               // [64][SCAN_LDB]  v_new with row i scaled by kdec_i, hi
+    uint32_t* vkl = vkh + DN_CHUNK * SCAN_LDB;                               //                  and lo
+    u64* bars = reinterpret_cast<u64*>(vkl + DN_CHUNK * SCAN_LDB);           // full1, full2, empty1, empty2
     const int h = blockIdx.x, vs = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t4 = lane & 3;
     const int v0 = vs * SCAN_VW;
@@ -572,7 +576,7 @@ static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(c
                 if (c > 0) scan_wait(empty2, (c - 1) & 1, err);
                 mbar_arrive_expect_tx(full2, SCAN_G2_BYTES);
                 bulk_load_1d(smem_u32(sk), &in.ks[0][0], DN_CHUNK * SCAN_LDT * 4, full2);
-                bulk_load_1d(smem_u32(sa), &in.aqk[0][0], DN_CHUNK * SCAN_LDQ * 4, full2);
+                bulk_load_1d(smem_u32(sa), &in.aqk[0][0], DN_CHUNK * (SCAN_LDQ + 1) * 4, full2);      // aqk and kdec
             }
         }
         return;
@@ -618,16 +622,22 @@ static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(c
                 for (int r = 0; r < 4; ++r) acc[nt][r] = sum_terms(a3[0][nt], r) + sum_terms(a3[1][nt], r);
         }
         if (warp < 4) {
-            // v_new = vprime - VP, stored split as the B operand of P2 and P3
+            // v_new = vprime - VP, stored split as the B operand of P2, and with row i scaled by exp(gc_last - gc_i) as the
+            // B operand of P3 (the scale arrives with group 2, requested a chunk ago)
+            scan_wait(full2, c & 1, err);
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
                     const int row = m0 + g + 8 * (r >> 1), col = nt * 8 + 2 * t4 + (r & 1);
+                    const float vn = svp[row * SCAN_VW + col] - acc[nt][r];
                     uint32_t hi, lo;
-                    tf32_split(svp[row * SCAN_VW + col] - acc[nt][r], hi, lo);
+                    tf32_split(vn, hi, lo);
                     vnh[row * SCAN_LDB + col] = hi;
                     vnl[row * SCAN_LDB + col] = lo;
+                    tf32_split(vn * skd[row], hi, lo);
+                    vkh[row * SCAN_LDB + col] = hi;
+                    vkl[row * SCAN_LDB + col] = lo;
                 }
         }
         __syncwarp();
@@ -663,30 +673,33 @@ static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(c
                     }
                 }
         }
-        // ---- P3 (all warps): S' = S exp(gc_last) + ks^T v_new; this warp owns state rows (keys) 16 warp .. 16 warp + 15 ----
+        // ---- P3 (all warps): S' = S exp(gc_last) + k^T (e v_new); this warp owns state rows (keys) 16 warp .. 16 warp + 15 ----
         {
             const int d0 = warp * 16;
-            float a3[2][2][3][4];
+            // k is exact in tf32, so each tile takes two mma (k x lo, k x hi of the scaled v_new) on separate accumulators
+            float a2[2][2][2][4];
 #pragma unroll
-            for (int i = 0; i < 48; ++i) a3[i / 24][(i / 12) & 1][(i >> 2) % 3][i & 3] = 0.f;
+            for (int i = 0; i < 32; ++i) a2[i >> 4][(i >> 3) & 1][(i >> 2) & 1][i & 3] = 0.f;
 #pragma unroll 2
             for (int k0 = 0; k0 < DN_CHUNK / 2; k0 += 8) {
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
                     const int kk = k0 + hf * (DN_CHUNK / 2);
-                    uint32_t ah[4], al[4];
-                    load_at_split(sk, SCAN_LDT, d0, kk, ah, al);
+                    uint32_t a[4];
+                    load_at_exact(sk, SCAN_LDT, d0, kk, a);
 #pragma unroll
                     for (int nt = 0; nt < 2; ++nt) {
                         const int bi0 = (kk + t4) * SCAN_LDB + nt * 8 + g, bi1 = bi0 + 4 * SCAN_LDB;
-                        mma_3xtf32_terms(a3[hf][nt], ah, al, vnh[bi0], vnh[bi1], vnl[bi0], vnl[bi1]);
+                        mma_tf32(a2[hf][nt][0], a, vkl[bi0], vkl[bi1]);
+                        mma_tf32(a2[hf][nt][1], a, vkh[bi0], vkh[bi1]);
                     }
                 }
             }
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-                for (int r = 0; r < 4; ++r) st[nt][r] = fmaf(st[nt][r], dec, sum_terms(a3[0][nt], r) + sum_terms(a3[1][nt], r));
+                for (int r = 0; r < 4; ++r)
+                    st[nt][r] = fmaf(st[nt][r], dec, (a2[0][nt][0][r] + a2[1][nt][0][r]) + (a2[0][nt][1][r] + a2[1][nt][1][r]));
             // the new state, split, for the next chunk's P1 (only this warp reads or writes these rows before the barrier)
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt)
