@@ -234,44 +234,54 @@ __device__ __forceinline__ void load_a_split(const float* A, int ld, int m0, int
     tf32_split(A[(m0 + g) * ld + k0 + t + 4], ah[2], al[2]);
     tf32_split(A[(m0 + g + 8) * ld + k0 + t + 4], ah[3], al[3]);
 }
-// A = M^T with M holding values that are exact in tf32 (bf16 inputs): the bits go to the mma as they are
-__device__ __forceinline__ void load_at_exact(const float* M, int ld, int m0, int k0, uint32_t (&a)[4]) {
-    const int g = (threadIdx.x & 31) >> 2, t = threadIdx.x & 3;
-    a[0] = __float_as_uint(M[(k0 + t) * ld + m0 + g]);
-    a[1] = __float_as_uint(M[(k0 + t) * ld + m0 + g + 8]);
-    a[2] = __float_as_uint(M[(k0 + t + 4) * ld + m0 + g]);
-    a[3] = __float_as_uint(M[(k0 + t + 4) * ld + m0 + g + 8]);
+// four 8 x 8 tiles of 16-bit elements from shared memory (each lane passes one row address), plain and transposed
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];" : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];" : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
 }
 
 // ---- chunk-local part of the gated delta rule: one CTA (16 warps) per (chunk, head) --------------
 // Per chunk of 64 tokens (zero padded): gc = cumsum(g); T = (I + tril((k beta) k^T * decay, -1))^-1 (a unit lower triangular
-// solve); vprime = T (v beta); kcd = T (k beta exp(gc)); aqk = tril(q k^T * decay).  f32 throughout; the four matrix products
-// (k k^T, q k^T, T v, T k) run on the tensor cores with q, k, v as exact tf32 operands (they are bf16 values) and only T split
-// hi + lo; the triangular solve runs on the CUDA cores in 16 x 16 blocks.
-// The record the scan kernel reads.  Its arrays have the row pitches of the scan's shared-memory operands (padded against
-// bank conflicts) and vprime is stored by 16-column slice, so that each operand of a scan CTA is ONE contiguous block
-// and moves with a single bulk copy; the pad columns are never read by an mma.
+// solve); vprime = T (v beta); aqk = tril(q k^T * decay).  f32 throughout; the three matrix products (k k^T, q k^T, T v) run
+// on the tensor cores with q, k, v as exact tf32 operands (they are bf16 values) and only T split hi + lo; the triangular
+// solve runs on the CUDA cores in 16 x 16 blocks.
+// The record the scan kernel reads.  Every one of its 8 value slices of a head reads the shared part of the record, so the
+// record is kept small: q and k stay the bf16 values they are, T and aqk keep only the 16-row tiles' columns up to the
+// diagonal block, and the product T (k beta exp(gc)) of the chunk-64 formulation is not formed at all (the scan multiplies
+// k S first, a 64 x 16 matrix, and T after).  Each group of arrays that lands together is contiguous, in the row pitches of
+// the scan's shared-memory operands, so it moves with one bulk copy; pad columns are never read.
 constexpr int SCAN_VW = 16;                 // value columns per scan CTA
-constexpr int SCAN_LDA = DN_K + 4;          // kcd, qs: row-major A operands, bank = 4 g + t
-constexpr int SCAN_LDT = DN_K + 8;          // ks: read as its transpose, bank = 8 t + g
-constexpr int SCAN_LDQ = DN_CHUNK + 4;      // aqk
-struct ChunkScratch {          // one record per (head, chunk), floats; every array starts on a 16-byte boundary
-    float vprime[DN_V / SCAN_VW][DN_CHUNK][SCAN_VW];
-    float kcd[DN_CHUNK][SCAN_LDA];
-    float qs[DN_CHUNK][SCAN_LDA];      // q / sqrt(128) * exp(gc_i): the scan's left operand of q S
-    float ks[DN_CHUNK][SCAN_LDT];      // k as read (bf16 values):   the scan's left operand of the state update, exact in tf32
-    float aqk[DN_CHUNK][SCAN_LDQ];
-    float kdec[DN_CHUNK];              // exp(gc_last - gc_i): the scan scales row i of v_new by it for the state update (follows aqk: one copy)
-    float eg_last[4];              // [0] = exp(gc_last)
+constexpr int SCAN_LDH = DN_K + 8;          // q, k as bf16 [token][dim]: 272-byte rows put the 8 rows of an ldmatrix tile in 8 bank groups
+// T and aqk: row tile m (16 rows) holds columns 0 .. 16 (m + 1) - 1 at pitch 16 (m + 1) + 8 floats (8 or 24 mod 32: the
+// 64-bit fragment loads of a half warp, rows g = 0..3, fall in different banks)
+__host__ __device__ constexpr int tri_pitch(int m) { return 16 * (m + 1) + 8; }
+__host__ __device__ constexpr int tri_off(int m) { return 128 * m * (m + 2); }
+constexpr int SCAN_TRI = tri_off(4);        // 3072 floats
+struct ChunkScratch {          // one record per (head, chunk); every array starts on a 16-byte boundary
+    float vprime[DN_V / SCAN_VW][DN_CHUNK][SCAN_VW];     // by 16-column slice: a scan CTA copies its own
+    bf16 q[DN_CHUNK][SCAN_LDH];        // copy 1: q and k as read (conv + SiLU + L2 norm output)
+    bf16 k[DN_CHUNK][SCAN_LDH];
+    float tmat[SCAN_TRI];              // copy 2: T, aqk and the four vectors
+    float aqk[SCAN_TRI];
+    float wsc[DN_CHUNK];               // beta_i exp(gc_i):       scales row i of k S
+    float dq[DN_CHUNK];                // exp(gc_i) / sqrt(128):  scales row i of q S
+    float kdec[DN_CHUNK];              // exp(gc_last - gc_i):    scales row i of v_new for the state update
+    float eg_last[4];                  // [0] = exp(gc_last)
 };
 static_assert(sizeof(ChunkScratch) % 16 == 0, "records must keep 16-byte alignment");
+constexpr uint32_t SCAN_QK_BYTES = 2 * DN_CHUNK * SCAN_LDH * 2, SCAN_TA_BYTES = (2 * SCAN_TRI + 3 * DN_CHUNK + 4) * 4,
+                   SCAN_VP_BYTES = DN_CHUNK * SCAN_VW * 4;
+static_assert(offsetof(ChunkScratch, k) == offsetof(ChunkScratch, q) + SCAN_QK_BYTES / 2 &&
+              offsetof(ChunkScratch, eg_last) + 16 == offsetof(ChunkScratch, tmat) + SCAN_TA_BYTES, "the copies assume this layout");
 
 constexpr int CL_THREADS = 512;
 constexpr float CL_QSCALE = 0.08838834764831845f;        // 1 / sqrt(128)
 constexpr int CL_LD = DN_K + 4;                          // q, k: A operands (row-major) and, for k, the transposed B operand: bank = 4 g + t
-constexpr int CL_LDB = DN_K + 8;                         // v beta, k beta exp(gc): B operands [token][dim]: bank = 8 t + g
-constexpr int CL_LDA = DN_CHUNK + 4;                     // T: A operand of the last two products
-constexpr int CHUNK_LOCAL_SMEM = (2 * DN_CHUNK * CL_LD + 2 * DN_CHUNK * CL_LDB + 2 * DN_CHUNK * CL_LDA + 3 * 256 + 3 * DN_CHUNK) * 4;
+constexpr int CL_LDB = DN_K + 8;                         // v: B operand [token][dim]: bank = 8 t + g
+constexpr int CL_LDA = DN_CHUNK + 4;                     // T: A operand of the last product
+constexpr int CHUNK_LOCAL_SMEM = (2 * DN_CHUNK * CL_LD + DN_CHUNK * CL_LDB + 2 * DN_CHUNK * CL_LDA + 3 * 256 + 3 * DN_CHUNK) * 4;
 
 static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(const bf16* __restrict__ qkv, const float* __restrict__ beta,
                                                                        const float* __restrict__ g, ChunkScratch* __restrict__ scratch,
@@ -281,8 +291,7 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
     float* sq = sm;                                  // [64][CL_LD]   q / sqrt(128)
     float* sk = sq + DN_CHUNK * CL_LD;               // [64][CL_LD]   k
     float* sv = sk + DN_CHUNK * CL_LD;               // [64][CL_LDB]  v
-    float* skb = sv + DN_CHUNK * CL_LDB;             // [64][CL_LDB]  k again, in the B-operand pitch
-    float* sa = skb + DN_CHUNK * CL_LDB;             // [64][CL_LDA]  N = -(k beta) k^T * decay, strictly lower
+    float* sa = sv + DN_CHUNK * CL_LDB;              // [64][CL_LDA]  N = -(k beta) k^T * decay, strictly lower
     float* sx = sa + DN_CHUNK * CL_LDA;              // [64][CL_LDA]  T = (I - N)^-1
     float* sw = sx + DN_CHUNK * CL_LDA;              // [3][16][16]   block products of the inversion
     float* sb = sw + 3 * 256;
@@ -308,7 +317,9 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
             vr = *reinterpret_cast<const uint4*>(row + 2 * DN_QK_SIZE);
         }
         // q and k stay the bf16 values they are (8 significant bits: exact as tf32 operands); the 1 / sqrt(128) of q is applied to
-        // the products below
+        // the products below.  The scan reads the same bf16 rows (zero for padding tokens).
+        *reinterpret_cast<uint4*>(&out.q[i][d]) = qr;
+        *reinterpret_cast<uint4*>(&out.k[i][d]) = kr;
         *reinterpret_cast<float4*>(sq + i * CL_LD + d) = make_float4(bf_lo(qr.x), bf_hi(qr.x), bf_lo(qr.y), bf_hi(qr.y));
         *reinterpret_cast<float4*>(sq + i * CL_LD + d + 4) = make_float4(bf_lo(qr.z), bf_hi(qr.z), bf_lo(qr.w), bf_hi(qr.w));
         *reinterpret_cast<float4*>(sk + i * CL_LD + d) = make_float4(bf_lo(kr.x), bf_hi(kr.x), bf_lo(kr.y), bf_hi(kr.y));
@@ -322,20 +333,15 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
         for (int i = 0; i < DN_CHUNK; ++i) { acc += sg[i]; sg[i] = acc; }
     }
     __syncthreads();
-    if (tid < DN_CHUNK) { se[tid] = expf(sg[tid]); out.kdec[tid] = expf(sg[DN_CHUNK - 1] - sg[tid]); }
-    __syncthreads();
-    {   // operands of the scan that depend on this chunk only; a copy of k in the B-operand pitch for the products below
-        const float g_last = sg[DN_CHUNK - 1];
-        for (int e = tid; e < DN_CHUNK * (DN_K / 4); e += CL_THREADS) {
-            const int i = e >> 5, d = (e & 31) * 4;
-            const float4 kv = *reinterpret_cast<const float4*>(sk + i * CL_LD + d), qv = *reinterpret_cast<const float4*>(sq + i * CL_LD + d);
-            const float ei = se[i];
-            *reinterpret_cast<float4*>(&out.qs[i][d]) = make_float4((qv.x * CL_QSCALE) * ei, (qv.y * CL_QSCALE) * ei, (qv.z * CL_QSCALE) * ei, (qv.w * CL_QSCALE) * ei);
-            *reinterpret_cast<float4*>(&out.ks[i][d]) = kv;
-            *reinterpret_cast<float4*>(skb + i * CL_LDB + d) = kv;
-        }
-        if (tid == 0) out.eg_last[0] = expf(g_last);
+    if (tid < DN_CHUNK) {            // the per-token factors of the scan
+        const float e = expf(sg[tid]);
+        se[tid] = e;
+        out.wsc[tid] = sb[tid] * e;
+        out.dq[tid] = CL_QSCALE * e;
+        out.kdec[tid] = expf(sg[DN_CHUNK - 1] - sg[tid]);
+        if (tid == 0) out.eg_last[0] = expf(sg[DN_CHUNK - 1]);
     }
+    __syncthreads();
     // ---- k k^T and q k^T (64 x 64 x 128): only the tiles on and below the diagonal.  A = rows of k (warps 0-7) or q (8-15),
     // B = k^T.  Eight warps share the 20 lower-triangular 16 x 8 ... tiles of one product: (row tile, first column tile, count)
     {
@@ -378,14 +384,14 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
                 for (int r = 0; r < 4; ++r) {
                     const int i = mt * 16 + gq + 8 * (r >> 1), j = (nt0 + n) * 8 + 2 * t4 + (r & 1);
                     const float dec = (j <= i) ? expf(sg[i] - sg[j]) : 0.f;
-                    if (is_q) out.aqk[i][j] = (j <= i) ? (acc[n][r] * CL_QSCALE) * dec : 0.f;
+                    if (is_q) out.aqk[tri_off(mt) + (i & 15) * tri_pitch(mt) + j] = (j <= i) ? (acc[n][r] * CL_QSCALE) * dec : 0.f;
                     else sa[i * CL_LDA + j] = (j < i) ? -((acc[n][r] * sb[i]) * dec) : 0.f;
                 }
-        // the tiles above the diagonal blocks were not computed: aqk and A are zero there (the forward substitution reads
-        // column entries above the diagonal and relies on their being zero)
+        // the tiles above the diagonal blocks were not computed: A is zero there (the forward substitution reads column
+        // entries above the diagonal and relies on their being zero); aqk does not store them
         for (int e = tid; e < DN_CHUNK * DN_CHUNK; e += CL_THREADS) {
             const int i = e >> 6, j = e & 63;
-            if ((j >> 4) > (i >> 4)) { out.aqk[i][j] = 0.f; sa[i * CL_LDA + j] = 0.f; }
+            if ((j >> 4) > (i >> 4)) sa[i * CL_LDA + j] = 0.f;
         }
     }
     __syncthreads();
@@ -457,74 +463,77 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
         }
         __syncthreads();
     }
-    // ---- vprime = T (v beta) (warps 0-7), kcd = T (k beta exp(gc)) (warps 8-15): 64 x 128 x 64 with T lower triangular.
-    // beta_j and beta_j exp(gc_j) belong to the summation index j, so they go into the left operand: T diag(beta) times the
-    // rows of v, T diag(beta exp(gc)) times the rows of k.  v and k are bf16 values, exact as tf32 operands, so only the
-    // left operand is split: two MMAs per tile and k-step instead of three, and no split of the right operand.
+    // ---- vprime = T (v beta): 64 x 128 x 64 with T lower triangular.  beta_j belongs to the summation index j, so it goes into
+    // the left operand: T diag(beta) times the rows of v.  v is bf16 values, exact as a tf32 operand, so only the left operand
+    // is split: two MMAs per tile and k-step instead of three.  T itself goes to the scan, tile rows up to the diagonal block.
     for (int e = tid; e < DN_CHUNK * DN_CHUNK; e += CL_THREADS) {
-        const int i = e >> 6, j = e & 63;
-        const float tij = (j >> 4) <= (i >> 4) ? sx[i * CL_LDA + j] : 0.f;
+        const int i = e >> 6, j = e & 63, m = i >> 4;
+        const bool in = (j >> 4) <= m;
+        const float tij = in ? sx[i * CL_LDA + j] : 0.f;
         sa[i * CL_LDA + j] = tij * sb[j];                  // N is no longer needed: its buffer holds T diag(beta)
-        sx[i * CL_LDA + j] = tij * (sb[j] * se[j]);
+        if (in) out.tmat[tri_off(m) + (i & 15) * tri_pitch(m) + j] = tij;
     }
     __syncthreads();
-    // A warp takes a quarter of the 128 columns and two row tiles whose k ranges add up to the same length: (0, 3) or (1, 2).
+    // A warp takes an eighth of the 128 columns and two row tiles whose k ranges add up to the same length: (0, 3) or (1, 2).
     {
-        const int u = warp & 7, nq = u & 3;
-        const bool to_vp = warp < 8;
-        const float* Bm = to_vp ? sv : skb;
-        const float* Am = to_vp ? sa : sx;
+        const int nq = warp & 7;
+        const bool outer = warp < 8;
 #pragma unroll
         for (int pass = 0; pass < 2; ++pass) {
-            const int mt = (u < 4) ? (pass ? 3 : 0) : (pass ? 2 : 1);
-            float acc2[4][2][4];
+            const int mt = outer ? (pass ? 3 : 0) : (pass ? 2 : 1);
+            float acc2[2][2][4];
 #pragma unroll
-            for (int n = 0; n < 4; ++n)
+            for (int n = 0; n < 2; ++n)
 #pragma unroll
                 for (int r = 0; r < 8; ++r) acc2[n][r >> 2][r & 3] = 0.f;
             for (int k0 = 0; k0 < 16 * (mt + 1); k0 += 8) {
                 uint32_t ah[4], al[4];
-                load_a_split(Am, CL_LDA, mt * 16, k0, ah, al);
+                load_a_split(sa, CL_LDA, mt * 16, k0, ah, al);
 #pragma unroll
-                for (int n = 0; n < 4; ++n) {
-                    const float* br = Bm + (k0 + t4) * CL_LDB + nq * 32 + n * 8 + gq;       // B(k, n) = Bm[token k][dim n]
+                for (int n = 0; n < 2; ++n) {
+                    const float* br = sv + (k0 + t4) * CL_LDB + nq * 16 + n * 8 + gq;       // B(k, n) = v[token k][dim n]
                     const uint32_t b0 = __float_as_uint(br[0]), b1 = __float_as_uint(br[4 * CL_LDB]);
                     mma_tf32(acc2[n][0], al, b0, b1);
                     mma_tf32(acc2[n][1], ah, b0, b1);
                 }
             }
 #pragma unroll
-            for (int n = 0; n < 4; ++n)
+            for (int n = 0; n < 2; ++n)
 #pragma unroll
-                for (int hr = 0; hr < 2; ++hr)
-                {
-                    const int i = mt * 16 + gq + 8 * hr, d = nq * 32 + n * 8 + 2 * t4;
-                    float* dst = to_vp ? &out.vprime[d / SCAN_VW][i][d % SCAN_VW] : &out.kcd[i][d];
-                    *reinterpret_cast<float2*>(dst) = make_float2(acc2[n][0][2 * hr] + acc2[n][1][2 * hr], acc2[n][0][2 * hr + 1] + acc2[n][1][2 * hr + 1]);
+                for (int hr = 0; hr < 2; ++hr) {
+                    const int i = mt * 16 + gq + 8 * hr, d = nq * 16 + n * 8 + 2 * t4;
+                    *reinterpret_cast<float2*>(&out.vprime[d / SCAN_VW][i][d % SCAN_VW]) =
+                        make_float2(acc2[n][0][2 * hr] + acc2[n][1][2 * hr], acc2[n][0][2 * hr + 1] + acc2[n][1][2 * hr + 1]);
                 }
         }
     }
 }
 
-// ---- scan over chunks: one CTA (8 warps) per (head, 16-wide slice of the value dimension) --------
-// Sequential over the chunks of a head; per chunk  v_new = vprime - kcd S,  out = qs S + aqk v_new,
-// S <- S exp(gc_last) + k^T (e v_new)  (S = state slice [128 k][16 v]).  All four products run on the tensor cores as
-// 3xTF32 mma.sync tiles (two terms where the left operand is exact):
-//   P1  warps 0-3: VP = kcd S, warps 4-7: IT = qs S      (64 x 128 x 16, one 16-row tile and both 8-column tiles per warp)
-//   P2  warps 4-7: out = IT + aqk v_new                   (64 x 64 x 16, lower-triangular: zero k-steps skipped)
-//   P3  all warps: S' = S exp(gc_last) + k^T (e v_new)    (128 x 64 x 16, one 16-row tile per warp; e_i = exp(gc_last - gc_i);
-//                                                          k is exact in tf32: two mma per tile instead of three)
-// The state slice lives in registers as the f32 accumulator fragment of P3 from chunk to chunk (no precision is lost to
-// the operand split); shared memory holds its hi / lo split as the B operand of the next chunk's P1, and v_new likewise.
-// The left operands are plain copies of what the chunk-local kernel wrote, in the layout it wrote them.  A ninth warp brings
-// them in with five bulk copies per chunk (completion counted on an mbarrier): group 1 = {kcd, qs, vprime slice}, group 2 =
-// {ks, aqk}, each refilled as soon as the eight compute warps have released its buffers; no compute warp issues a copy.
+// ---- scan over chunks: one CTA (8 compute warps + a copy warp) per (head, 16-wide slice of the value dimension) --------
+// Sequential over the chunks of a head; with S the state slice [128 k][16 v], per chunk
+//   W = w (k S),  v_new = vprime - T W,  out = d (q S) + aqk v_new,  S <- S exp(gc_last) + k^T (e v_new)
+// (w_i = beta_i exp(gc_i), d_i = exp(gc_i) / sqrt(128), e_i = exp(gc_last - gc_i); T W equals the chunk-64 formulation's
+// (T (k beta exp(gc))) S with the products taken in the other order).  All products are mma.sync tf32 tiles with the
+// accuracy of f32: q and k are bf16 values, exact as tf32 operands, so only the other operand is split hi + lo (two mma
+// per tile); T, aqk, W and v_new are split on both sides (three mma).  The eight warps form a 4 x 2 grid (16-token row tile
+// x 8-column tile):
+//   P1  warp (mt, nt): k S and q S tiles             (16 x 128 x 8 each; A fragments by ldmatrix from the bf16 rows)
+//   P1b the same warp:  T W tile -> v_new tile        (lower triangular: row tile mt sums over 16 (mt + 1) tokens)
+//   P2  the same warp:  out tile = d (q S) + aqk v_new
+//   P3  warp w: state rows 16 w .. 16 w + 15          (128 x 64 x 16; A = k^T by transposing ldmatrix)
+// Within a k-step of 8 the mma's k index t stands for element 2 t and t + 4 for element 2 t + 1, so that a bf16 pair (or a
+// float2) is one fragment pair; the B operands are read by the same rule.  The state slice lives in registers as the f32
+// accumulator fragment of P3 from chunk to chunk; shared memory holds its hi / lo split as the B operand of the next
+// chunk's P1.  The copy warp brings each chunk's operands in with three bulk copies (completion counted on an mbarrier)
+// into one of two stages, a chunk ahead of the compute warps.  Row tiles of the last chunk that hold only padding are
+// skipped.
 constexpr int SCAN_CONS = 256;              // compute threads
 constexpr int SCAN_THREADS = SCAN_CONS + 32;
-constexpr int SCAN_LDB = SCAN_VW + 8;       // B operands (state and v_new, hi and lo): bank = 24 t + g
-constexpr int CHUNK_SCAN_SMEM = (2 * DN_CHUNK * SCAN_LDA + DN_CHUNK * SCAN_LDT + DN_CHUNK * SCAN_LDQ + DN_CHUNK + DN_CHUNK * SCAN_VW +
-                                 2 * DN_K * SCAN_LDB + 4 * DN_CHUNK * SCAN_LDB) * 4 + 64;
-constexpr uint32_t SCAN_G1_BYTES = DN_CHUNK * (2 * SCAN_LDA + SCAN_VW) * 4, SCAN_G2_BYTES = DN_CHUNK * (SCAN_LDT + SCAN_LDQ + 1) * 4;
+constexpr int SCAN_LDB = SCAN_VW + 4;       // B operands (state, W, v_new; hi and lo): rows 2 t, 2 t + 1: bank = 8 t + g
+constexpr int SCAN_NSTAGE = 2;
+constexpr uint32_t SCAN_STAGE_BYTES = SCAN_QK_BYTES + SCAN_TA_BYTES + SCAN_VP_BYTES;
+constexpr int CHUNK_SCAN_SMEM = SCAN_NSTAGE * SCAN_STAGE_BYTES + (2 * DN_K + 6 * DN_CHUNK) * SCAN_LDB * 4 + 64;
+static_assert(SCAN_STAGE_BYTES % 128 == 0 || SCAN_STAGE_BYTES % 16 == 0, "stages keep 16-byte alignment");
 constexpr unsigned SCAN_WAIT_LIMIT = 1u << 26;      // a bounded wait: a copy that never lands ends the loop instead of hanging
 
 __device__ __forceinline__ void scan_wait(uint32_t bar, uint32_t parity, int* err) {
@@ -533,52 +542,63 @@ __device__ __forceinline__ void scan_wait(uint32_t bar, uint32_t parity, int* er
         if (++it >= SCAN_WAIT_LIMIT) { atomicCAS(err, 0, (int)ERR_BARRIER_TIMEOUT); return; }
 }
 __device__ __forceinline__ void scan_cons_sync() { asm volatile("bar.sync 1, %0;" ::"n"(SCAN_CONS) : "memory"); }
+// 16 x 8 (x 16 (mt + 1)) product of a row tile of a packed lower-triangular matrix (T or aqk) with a split B operand
+__device__ __forceinline__ void scan_tri_product(float (&a3)[3][4], const float* tile, int pitch, int klen, const uint32_t* bh, const uint32_t* bl,
+                                                 int col, int g, int t4) {
+    const float* r0 = tile + g * pitch + 2 * t4;
+    const float* r1 = r0 + 8 * pitch;
+    for (int j0 = 0; j0 < klen; j0 += 8) {
+        const float2 x0 = *reinterpret_cast<const float2*>(r0 + j0), x1 = *reinterpret_cast<const float2*>(r1 + j0);
+        uint32_t ah[4], al[4];
+        tf32_split(x0.x, ah[0], al[0]);
+        tf32_split(x1.x, ah[1], al[1]);
+        tf32_split(x0.y, ah[2], al[2]);
+        tf32_split(x1.y, ah[3], al[3]);
+        const int bi0 = (j0 + 2 * t4) * SCAN_LDB + col, bi1 = bi0 + SCAN_LDB;
+        mma_3xtf32_terms(a3, ah, al, bh[bi0], bh[bi1], bl[bi0], bl[bi1]);
+    }
+}
 
 static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(const ChunkScratch* __restrict__ scratch, bf16* __restrict__ core_out,
                                                                         float* __restrict__ state_out, int S, int nchunks, int* __restrict__ err) {
     pdl_wait();
-    extern __shared__ __align__(16) float sm[];
-    float* skcd = sm;                                   // [64][SCAN_LDA]
-    float* sq = skcd + DN_CHUNK * SCAN_LDA;             // [64][SCAN_LDA]
-    float* sk = sq + DN_CHUNK * SCAN_LDA;               // [64][SCAN_LDT]
-    float* sa = sk + DN_CHUNK * SCAN_LDT;               // [64][SCAN_LDQ]
-    float* skd = sa + DN_CHUNK * SCAN_LDQ;              // [64] exp(gc_last - gc_i), lands with aqk
-    float* svp = skd + DN_CHUNK;                        // [64][16]
-    uint32_t* sth = reinterpret_cast<uint32_t*>(svp + DN_CHUNK * SCAN_VW);   // [128][SCAN_LDB] state, tf32 hi
-    uint32_t* stl = sth + DN_K * SCAN_LDB;                                   //                  state, tf32 lo
-    uint32_t* vnh = stl + DN_K * SCAN_LDB;                                   // [64][SCAN_LDB]  v_new, tf32 hi
-    uint32_t* vnl = vnh + DN_CHUNK * SCAN_LDB;                               //                  v_new, tf32 lo
-    uint32_t* vkh = vnl + DN_CHUNK * SCAN_LDB;                               // [64][SCAN_LDB]  v_new with row i scaled by kdec_i, hi
-    uint32_t* vkl = vkh + DN_CHUNK * SCAN_LDB;                               //                  and lo
-    u64* bars = reinterpret_cast<u64*>(vkl + DN_CHUNK * SCAN_LDB);           // full1, full2, empty1, empty2
+    extern __shared__ __align__(128) unsigned char scan_sm[];
+    uint32_t* sth = reinterpret_cast<uint32_t*>(scan_sm + SCAN_NSTAGE * SCAN_STAGE_BYTES);     // [128][SCAN_LDB] state, tf32 hi
+    uint32_t* stl = sth + DN_K * SCAN_LDB;                                                     //                  state, tf32 lo
+    uint32_t* swh = stl + DN_K * SCAN_LDB;                                                     // [64][SCAN_LDB]  W, hi
+    uint32_t* swl = swh + DN_CHUNK * SCAN_LDB;                                                 //                  W, lo
+    uint32_t* vnh = swl + DN_CHUNK * SCAN_LDB;                                                 // [64][SCAN_LDB]  v_new, hi
+    uint32_t* vnl = vnh + DN_CHUNK * SCAN_LDB;                                                 //                  v_new, lo
+    uint32_t* vkh = vnl + DN_CHUNK * SCAN_LDB;                                                 // [64][SCAN_LDB]  e v_new, hi
+    uint32_t* vkl = vkh + DN_CHUNK * SCAN_LDB;                                                 //                  e v_new, lo
+    u64* bars = reinterpret_cast<u64*>(vkl + DN_CHUNK * SCAN_LDB);                             // full[2], empty[2]
     const int h = blockIdx.x, vs = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t4 = lane & 3;
     const int v0 = vs * SCAN_VW;
-    const uint32_t full1 = smem_u32(bars), full2 = smem_u32(bars + 1), empty1 = smem_u32(bars + 2), empty2 = smem_u32(bars + 3);
+    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + SCAN_NSTAGE);
     if (tid == 0) {
-        mbar_init(full1, 1); mbar_init(full2, 1);
-        mbar_init(empty1, SCAN_CONS / 32); mbar_init(empty2, SCAN_CONS / 32);     // one arrival per compute warp
+        for (int i = 0; i < SCAN_NSTAGE; ++i) {
+            mbar_init(full0 + 8 * i, 1);
+            mbar_init(empty0 + 8 * i, SCAN_CONS / 32);       // one arrival per compute warp
+        }
         mbar_fence_init();
     }
     for (int e = tid; e < 2 * DN_K * SCAN_LDB; e += SCAN_THREADS) sth[e] = 0u;          // state = 0 (hi and lo)
     __syncthreads();
 
     if (warp == SCAN_CONS / 32) {
-        // ---- producer warp (one lane issues) ----
-        for (int c = 0; c < nchunks; ++c) {
-            const ChunkScratch& in = scratch[(size_t)h * nchunks + c];
-            if (lane == 0) {
-                if (c > 0) scan_wait(empty1, (c - 1) & 1, err);
-                mbar_arrive_expect_tx(full1, SCAN_G1_BYTES);
-                bulk_load_1d(smem_u32(skcd), &in.kcd[0][0], DN_CHUNK * SCAN_LDA * 4, full1);
-                bulk_load_1d(smem_u32(sq), &in.qs[0][0], DN_CHUNK * SCAN_LDA * 4, full1);
-                bulk_load_1d(smem_u32(svp), &in.vprime[vs][0][0], DN_CHUNK * SCAN_VW * 4, full1);
-                if (c > 0) scan_wait(empty2, (c - 1) & 1, err);
-                mbar_arrive_expect_tx(full2, SCAN_G2_BYTES);
-                bulk_load_1d(smem_u32(sk), &in.ks[0][0], DN_CHUNK * SCAN_LDT * 4, full2);
-                bulk_load_1d(smem_u32(sa), &in.aqk[0][0], DN_CHUNK * (SCAN_LDQ + 1) * 4, full2);      // aqk and kdec
+        // ---- copy warp (one lane issues), one chunk ahead ----
+        if (lane == 0)
+            for (int c = 0; c < nchunks; ++c) {
+                const ChunkScratch& in = scratch[(size_t)h * nchunks + c];
+                const int sg = c % SCAN_NSTAGE, use = c / SCAN_NSTAGE;
+                if (use > 0) scan_wait(empty0 + 8 * sg, (use - 1) & 1, err);
+                const uint32_t full = full0 + 8 * sg, dst = smem_u32(scan_sm) + sg * SCAN_STAGE_BYTES;
+                mbar_arrive_expect_tx(full, SCAN_STAGE_BYTES);
+                bulk_load_1d(dst, &in.q[0][0], SCAN_QK_BYTES, full);
+                bulk_load_1d(dst + SCAN_QK_BYTES, &in.tmat[0], SCAN_TA_BYTES, full);
+                bulk_load_1d(dst + SCAN_QK_BYTES + SCAN_TA_BYTES, &in.vprime[vs][0][0], SCAN_VP_BYTES, full);
             }
-        }
         return;
     }
 
@@ -588,141 +608,152 @@ static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(c
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int r = 0; r < 4; ++r) st[nt][r] = 0.f;
+    // the warp's tile of the 64 x 16 products: the two warps of a scheduler (warp and warp + 4) take row tiles mt and 3 - mt,
+    // whose triangular products add up to the same length
+    const int nt = warp >> 2, mt = nt ? 3 - (warp & 3) : (warp & 3), m0 = mt * 16, col = nt * 8 + g;
+    // ldmatrix row addresses (bytes from the start of q or k): P1 reads 16 rows x 16 columns, P3 16 tokens x 16 dims transposed
+    const uint32_t a_off = ((m0 + (lane & 7) + 8 * ((lane >> 3) & 1)) * SCAN_LDH + 8 * (lane >> 4)) * 2;
+    const uint32_t t_off = (((lane & 7) + 8 * (lane >> 4)) * SCAN_LDH + warp * 16 + 8 * ((lane >> 3) & 1)) * 2;
 
     for (int c = 0; c < nchunks; ++c) {
         const int t0 = c * DN_CHUNK;
-        const float dec = scratch[(size_t)h * nchunks + c].eg_last[0];
-        scan_wait(full1, c & 1, err);                                       // group 1 of this chunk has landed
-        // ---- P1: VP = kcd S (warps 0-3), IT = qs S (warps 4-7) ----
-        const int mt = warp & 3, m0 = mt * 16;
-        float acc[2][4];
-        {
-            // two halves of the k range x three terms: six independent accumulator chains per column tile
-            float a3[2][2][3][4];
+        const int sg = c % SCAN_NSTAGE;
+        const unsigned char* stage = scan_sm + sg * SCAN_STAGE_BYTES;
+        const uint32_t sq_a = smem_u32(stage), sk_a = sq_a + SCAN_QK_BYTES / 2;
+        const float* sT = reinterpret_cast<const float*>(stage + SCAN_QK_BYTES);
+        const float* sA = sT + SCAN_TRI;
+        const float* swsc = sA + SCAN_TRI;
+        const float* sdq = swsc + DN_CHUNK;
+        const float* skd = sdq + DN_CHUNK;
+        const float* seg = skd + DN_CHUNK;
+        const float* svp = seg + 4;
+        const int valid = min(DN_CHUNK, S - t0);
+        const bool live = mt * 16 < valid;                    // this row tile holds at least one token
+        const int kmax = (valid + 7) & ~7;                    // tokens the state update sums over, in k-steps
+        scan_wait(full0 + 8 * sg, (c / SCAN_NSTAGE) & 1, err);            // this chunk's operands have landed
+        const float dec = seg[0];
+        // ---- P1: tiles of k S and q S ----
+        float it[4] = {0.f, 0.f, 0.f, 0.f};
+        if (live) {
+            float ks2[2][2][4], it2[2][2][4];                // [half of the k range][lo / hi term]
 #pragma unroll
-            for (int i = 0; i < 48; ++i) a3[i / 24][(i / 12) & 1][(i >> 2) % 3][i & 3] = 0.f;
-            const float* A = (warp < 4) ? skcd : sq;
+            for (int i = 0; i < 16; ++i) { ks2[i >> 3][(i >> 2) & 1][i & 3] = 0.f; it2[i >> 3][(i >> 2) & 1][i & 3] = 0.f; }
 #pragma unroll 2
-            for (int k0 = 0; k0 < DN_K / 2; k0 += 8) {
+            for (int c0 = 0; c0 < DN_K / 2; c0 += 16) {
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
-                    const int kk = k0 + hf * (DN_K / 2);
-                    uint32_t ah[4], al[4];
-                    load_a_split(A, SCAN_LDA, m0, kk, ah, al);
+                    const int cc = c0 + hf * (DN_K / 2);
+                    uint32_t rq[4], rk[4];
+                    ldmatrix_x4(rk, sk_a + a_off + cc * 2);
+                    ldmatrix_x4(rq, sq_a + a_off + cc * 2);
 #pragma unroll
-                    for (int nt = 0; nt < 2; ++nt) {
-                        const int bi0 = (kk + t4) * SCAN_LDB + nt * 8 + g, bi1 = bi0 + 4 * SCAN_LDB;
-                        mma_3xtf32_terms(a3[hf][nt], ah, al, sth[bi0], sth[bi1], stl[bi0], stl[bi1]);
+                    for (int s2 = 0; s2 < 2; ++s2) {
+                        const uint32_t ak[4] = {rk[2 * s2] << 16, rk[2 * s2 + 1] << 16, rk[2 * s2] & 0xffff0000u, rk[2 * s2 + 1] & 0xffff0000u};
+                        const uint32_t aq[4] = {rq[2 * s2] << 16, rq[2 * s2 + 1] << 16, rq[2 * s2] & 0xffff0000u, rq[2 * s2 + 1] & 0xffff0000u};
+                        const int bi0 = (cc + 8 * s2 + 2 * t4) * SCAN_LDB + col, bi1 = bi0 + SCAN_LDB;
+                        const uint32_t bh0 = sth[bi0], bh1 = sth[bi1], bl0 = stl[bi0], bl1 = stl[bi1];
+                        mma_tf32(ks2[hf][0], ak, bl0, bl1);
+                        mma_tf32(it2[hf][0], aq, bl0, bl1);
+                        mma_tf32(ks2[hf][1], ak, bh0, bh1);
+                        mma_tf32(it2[hf][1], aq, bh0, bh1);
                     }
                 }
             }
+            // W = w (k S), split, as the B operand of P1b; d (q S) stays in registers for P2
 #pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                for (int r = 0; r < 4; ++r) acc[nt][r] = sum_terms(a3[0][nt], r) + sum_terms(a3[1][nt], r);
+            for (int r = 0; r < 4; ++r) {
+                const int row = m0 + g + 8 * (r >> 1);
+                const float w = ((ks2[0][0][r] + ks2[1][0][r]) + (ks2[0][1][r] + ks2[1][1][r])) * swsc[row];
+                it[r] = ((it2[0][0][r] + it2[1][0][r]) + (it2[0][1][r] + it2[1][1][r])) * sdq[row];
+                uint32_t hi, lo;
+                tf32_split(w, hi, lo);
+                swh[row * SCAN_LDB + nt * 8 + 2 * t4 + (r & 1)] = hi;
+                swl[row * SCAN_LDB + nt * 8 + 2 * t4 + (r & 1)] = lo;
+            }
         }
-        if (warp < 4) {
-            // v_new = vprime - VP, stored split as the B operand of P2, and with row i scaled by exp(gc_last - gc_i) as the
-            // B operand of P3 (the scale arrives with group 2, requested a chunk ago)
-            scan_wait(full2, c & 1, err);
+        scan_cons_sync();                                              // W complete
+        // ---- P1b: v_new = vprime - T W, stored split, plain for P2 and with row i scaled by e_i for P3 ----
+        if (live) {
+            float a3[3][4];
 #pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
+            for (int i = 0; i < 12; ++i) a3[i >> 2][i & 3] = 0.f;
+            scan_tri_product(a3, sT + tri_off(mt), tri_pitch(mt), 16 * (mt + 1), swh, swl, col, g, t4);
 #pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    const int row = m0 + g + 8 * (r >> 1), col = nt * 8 + 2 * t4 + (r & 1);
-                    const float vn = svp[row * SCAN_VW + col] - acc[nt][r];
-                    uint32_t hi, lo;
-                    tf32_split(vn, hi, lo);
-                    vnh[row * SCAN_LDB + col] = hi;
-                    vnl[row * SCAN_LDB + col] = lo;
-                    tf32_split(vn * skd[row], hi, lo);
-                    vkh[row * SCAN_LDB + col] = hi;
-                    vkl[row * SCAN_LDB + col] = lo;
-                }
+            for (int r = 0; r < 4; ++r) {
+                const int row = m0 + g + 8 * (r >> 1), cv = nt * 8 + 2 * t4 + (r & 1);
+                const float vn = svp[row * SCAN_VW + cv] - sum_terms(a3, r);
+                uint32_t hi, lo;
+                tf32_split(vn, hi, lo);
+                vnh[row * SCAN_LDB + cv] = hi;
+                vnl[row * SCAN_LDB + cv] = lo;
+                tf32_split(vn * skd[row], hi, lo);
+                vkh[row * SCAN_LDB + cv] = hi;
+                vkl[row * SCAN_LDB + cv] = lo;
+            }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty1, 1);                         // this warp is done with kcd / qs / vprime
         scan_cons_sync();                                              // v_new complete
-        scan_wait(full2, c & 1, err);                                       // group 2 of this chunk has landed
-        // ---- P2 (warps 4-7): out = IT + aqk v_new; aqk is lower triangular, so row tile mt needs tokens j < 16 (mt + 1) only ----
-        if (warp >= 4) {
-            float a3[2][3][4];
+        // ---- P2: out = d (q S) + aqk v_new ----
+        if (live) {
+            float a3[3][4];
 #pragma unroll
-            for (int i = 0; i < 24; ++i) a3[i / 12][(i >> 2) % 3][i & 3] = 0.f;
-            for (int k0 = 0; k0 < 16 * (mt + 1); k0 += 8) {
-                uint32_t ah[4], al[4];
-                load_a_split(sa, SCAN_LDQ, m0, k0, ah, al);
+            for (int i = 0; i < 12; ++i) a3[i >> 2][i & 3] = 0.f;
+            scan_tri_product(a3, sA + tri_off(mt), tri_pitch(mt), 16 * (mt + 1), vnh, vnl, col, g, t4);
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
-                    const int bi0 = (k0 + t4) * SCAN_LDB + nt * 8 + g, bi1 = bi0 + 4 * SCAN_LDB;
-                    mma_3xtf32_terms(a3[nt], ah, al, vnh[bi0], vnh[bi1], vnl[bi0], vnl[bi1]);
+            for (int hr = 0; hr < 2; ++hr) {
+                const int tok = t0 + m0 + g + 8 * hr;
+                if (tok < S) {
+                    bf16* dst = core_out + (size_t)tok * DN_V_SIZE + h * DN_V + v0 + nt * 8 + 2 * t4;
+                    *reinterpret_cast<__nv_bfloat162*>(dst) =
+                        __halves2bfloat162(f2bf(it[2 * hr] + sum_terms(a3, 2 * hr)), f2bf(it[2 * hr + 1] + sum_terms(a3, 2 * hr + 1)));
                 }
             }
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                for (int r = 0; r < 4; ++r) acc[nt][r] += sum_terms(a3[nt], r);
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                for (int hr = 0; hr < 2; ++hr) {
-                    const int tok = t0 + m0 + g + 8 * hr;
-                    if (tok < S) {
-                        bf16* dst = core_out + (size_t)tok * DN_V_SIZE + h * DN_V + v0 + nt * 8 + 2 * t4;
-                        *reinterpret_cast<__nv_bfloat162*>(dst) = __halves2bfloat162(f2bf(acc[nt][2 * hr]), f2bf(acc[nt][2 * hr + 1]));
-                    }
-                }
         }
-        // ---- P3 (all warps): S' = S exp(gc_last) + k^T (e v_new); this warp owns state rows (keys) 16 warp .. 16 warp + 15 ----
+        // ---- P3: S' = S exp(gc_last) + k^T (e v_new); this warp owns state rows (keys) 16 warp .. 16 warp + 15 ----
         {
-            const int d0 = warp * 16;
-            // k is exact in tf32, so each tile takes two mma (k x lo, k x hi of the scaled v_new) on separate accumulators
-            float a2[2][2][2][4];
+            float a2[2][2][4];                                   // [column tile][lo / hi term]
 #pragma unroll
-            for (int i = 0; i < 32; ++i) a2[i >> 4][(i >> 3) & 1][(i >> 2) & 1][i & 3] = 0.f;
+            for (int i = 0; i < 16; ++i) a2[i >> 3][(i >> 2) & 1][i & 3] = 0.f;
 #pragma unroll 2
-            for (int k0 = 0; k0 < DN_CHUNK / 2; k0 += 8) {
+            for (int j0 = 0; j0 < kmax; j0 += 16) {
+                uint32_t rk[4];
+                ldmatrix_x4_trans(rk, sk_a + t_off + j0 * (SCAN_LDH * 2));
 #pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-                    const int kk = k0 + hf * (DN_CHUNK / 2);
-                    uint32_t a[4];
-                    load_at_exact(sk, SCAN_LDT, d0, kk, a);
+                for (int s2 = 0; s2 < 2; ++s2) {
+                    const int jj = j0 + 8 * s2;
+                    if (jj >= kmax) continue;                        // padding tokens add nothing (uniform over the CTA)
+                    const uint32_t a[4] = {rk[2 * s2] << 16, rk[2 * s2 + 1] << 16, rk[2 * s2] & 0xffff0000u, rk[2 * s2 + 1] & 0xffff0000u};
 #pragma unroll
-                    for (int nt = 0; nt < 2; ++nt) {
-                        const int bi0 = (kk + t4) * SCAN_LDB + nt * 8 + g, bi1 = bi0 + 4 * SCAN_LDB;
-                        mma_tf32(a2[hf][nt][0], a, vkl[bi0], vkl[bi1]);
-                        mma_tf32(a2[hf][nt][1], a, vkh[bi0], vkh[bi1]);
+                    for (int n2 = 0; n2 < 2; ++n2) {
+                        const int bi0 = (jj + 2 * t4) * SCAN_LDB + n2 * 8 + g, bi1 = bi0 + SCAN_LDB;
+                        mma_tf32(a2[n2][0], a, vkl[bi0], vkl[bi1]);
+                        mma_tf32(a2[n2][1], a, vkh[bi0], vkh[bi1]);
                     }
                 }
             }
+            // the new state, in registers and split for the next chunk's P1
 #pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                for (int r = 0; r < 4; ++r)
-                    st[nt][r] = fmaf(st[nt][r], dec, (a2[0][nt][0][r] + a2[1][nt][0][r]) + (a2[0][nt][1][r] + a2[1][nt][1][r]));
-            // the new state, split, for the next chunk's P1 (only this warp reads or writes these rows before the barrier)
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
+            for (int n2 = 0; n2 < 2; ++n2)
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
-                    const int row = d0 + g + 8 * (r >> 1), col = nt * 8 + 2 * t4 + (r & 1);
+                    st[n2][r] = fmaf(st[n2][r], dec, a2[n2][0][r] + a2[n2][1][r]);
+                    const int row = warp * 16 + g + 8 * (r >> 1), cv = n2 * 8 + 2 * t4 + (r & 1);
                     uint32_t hi, lo;
-                    tf32_split(st[nt][r], hi, lo);
-                    sth[row * SCAN_LDB + col] = hi;
-                    stl[row * SCAN_LDB + col] = lo;
+                    tf32_split(st[n2][r], hi, lo);
+                    sth[row * SCAN_LDB + cv] = hi;
+                    stl[row * SCAN_LDB + cv] = lo;
                 }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(empty2, 1);                         // this warp is done with aqk / ks
-        scan_cons_sync();                                              // the new state split is complete; v_new may be overwritten
+        if (lane == 0) mbar_arrive(empty0 + 8 * sg, 1);                // this warp is done with the stage
+        scan_cons_sync();                                              // the new state split is complete; W and v_new may be overwritten
     }
     // final state in the reference layout [head][v][k], from the f32 registers
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
+    for (int n2 = 0; n2 < 2; ++n2)
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-            const int d = warp * 16 + g + 8 * (r >> 1), v = nt * 8 + 2 * t4 + (r & 1);
-            state_out[((size_t)h * DN_V + v0 + v) * DN_K + d] = st[nt][r];
+            const int d = warp * 16 + g + 8 * (r >> 1), v = n2 * 8 + 2 * t4 + (r & 1);
+            state_out[((size_t)h * DN_V + v0 + v) * DN_K + d] = st[n2][r];
         }
 }
 
