@@ -234,14 +234,6 @@ __device__ __forceinline__ void load_a_split(const float* A, int ld, int m0, int
     tf32_split(A[(m0 + g) * ld + k0 + t + 4], ah[2], al[2]);
     tf32_split(A[(m0 + g + 8) * ld + k0 + t + 4], ah[3], al[3]);
 }
-// four 8 x 8 tiles of 16-bit elements from shared memory (each lane passes one row address), plain and transposed
-__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];" : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
-}
-__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t addr) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];" : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
-}
-
 // ---- chunk-local part of the gated delta rule: one CTA (16 warps) per (chunk, head) --------------
 // Per chunk of 64 tokens (zero padded): gc = cumsum(g); T = (I + tril((k beta) k^T * decay, -1))^-1 (a unit lower triangular
 // solve); vprime = T (v beta); aqk = tril(q k^T * decay).  f32 throughout; the three matrix products (k k^T, q k^T, T v) run
@@ -250,10 +242,11 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t add
 // The record the scan kernel reads.  Every one of its 8 value slices of a head reads the shared part of the record, so the
 // record is kept small: q and k stay the bf16 values they are, T and aqk keep only the 16-row tiles' columns up to the
 // diagonal block, and the product T (k beta exp(gc)) of the chunk-64 formulation is not formed at all (the scan multiplies
-// k S first, a 64 x 16 matrix, and T after).  Each group of arrays that lands together is contiguous, in the row pitches of
-// the scan's shared-memory operands, so it moves with one bulk copy; pad columns are never read.
+// k S first, a 64 x 16 matrix, and T after).  q and k are stored as the scan's tcgen05 operands, in the K-major 128-byte-swizzle
+// layout the MMA reads (rows of 128 bytes, the 16-byte unit u of row r at position u ^ (r & 7)): qk = the 128 x 128 left operand
+// [k rows; q rows] of (k S, q S) as two blocks of 64 dims, kt = k^T (128 dims x 64 tokens), the left operand of the state
+// update.  Each group of arrays that lands together is contiguous, so it moves with one bulk copy; pad columns are never read.
 constexpr int SCAN_VW = 16;                 // value columns per scan CTA
-constexpr int SCAN_LDH = DN_K + 8;          // q, k as bf16 [token][dim]: 272-byte rows put the 8 rows of an ldmatrix tile in 8 bank groups
 // T and aqk: row tile m (16 rows) holds columns 0 .. 16 (m + 1) - 1 at pitch 16 (m + 1) + 8 floats (8 or 24 mod 32: the
 // 64-bit fragment loads of a half warp, rows g = 0..3, fall in different banks)
 __host__ __device__ constexpr int tri_pitch(int m) { return 16 * (m + 1) + 8; }
@@ -261,8 +254,8 @@ __host__ __device__ constexpr int tri_off(int m) { return 128 * m * (m + 2); }
 constexpr int SCAN_TRI = tri_off(4);        // 3072 floats
 struct ChunkScratch {          // one record per (head, chunk); every array starts on a 16-byte boundary
     float vprime[DN_V / SCAN_VW][DN_CHUNK][SCAN_VW];     // by 16-column slice: a scan CTA copies its own
-    bf16 q[DN_CHUNK][SCAN_LDH];        // copy 1: q and k as read (conv + SiLU + L2 norm output)
-    bf16 k[DN_CHUNK][SCAN_LDH];
+    bf16 qk[2][2 * DN_CHUNK][64];      // copy 1: [block of 64 dims][k tokens, then q tokens][dim], swizzled
+    bf16 kt[DN_K][DN_CHUNK];           //         [dim][token], swizzled
     float tmat[SCAN_TRI];              // copy 2: T, aqk and the four vectors
     float aqk[SCAN_TRI];
     float wsc[DN_CHUNK];               // beta_i exp(gc_i):       scales row i of k S
@@ -271,10 +264,12 @@ struct ChunkScratch {          // one record per (head, chunk); every array star
     float eg_last[4];                  // [0] = exp(gc_last)
 };
 static_assert(sizeof(ChunkScratch) % 16 == 0, "records must keep 16-byte alignment");
-constexpr uint32_t SCAN_QK_BYTES = 2 * DN_CHUNK * SCAN_LDH * 2, SCAN_TA_BYTES = (2 * SCAN_TRI + 3 * DN_CHUNK + 4) * 4,
-                   SCAN_VP_BYTES = DN_CHUNK * SCAN_VW * 4;
-static_assert(offsetof(ChunkScratch, k) == offsetof(ChunkScratch, q) + SCAN_QK_BYTES / 2 &&
+constexpr uint32_t SCAN_QK_BYTES = 2 * 2 * DN_CHUNK * 64 * 2, SCAN_KT_BYTES = DN_K * DN_CHUNK * 2,
+                   SCAN_TA_BYTES = (2 * SCAN_TRI + 3 * DN_CHUNK + 4) * 4, SCAN_VP_BYTES = DN_CHUNK * SCAN_VW * 4;
+static_assert(offsetof(ChunkScratch, kt) == offsetof(ChunkScratch, qk) + SCAN_QK_BYTES &&
               offsetof(ChunkScratch, eg_last) + 16 == offsetof(ChunkScratch, tmat) + SCAN_TA_BYTES, "the copies assume this layout");
+// byte offset of the 16-byte unit holding elements col .. col + 7 of row `row` in a swizzled block of 128-byte rows
+__host__ __device__ constexpr uint32_t sw128_off(int row, int col) { return (uint32_t)row * 128u + ((uint32_t)((col >> 3) ^ (row & 7)) << 4); }
 
 constexpr int CL_THREADS = 512;
 constexpr float CL_QSCALE = 0.08838834764831845f;        // 1 / sqrt(128)
@@ -318,8 +313,11 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
         }
         // q and k stay the bf16 values they are (8 significant bits: exact as tf32 operands); the 1 / sqrt(128) of q is applied to
         // the products below.  The scan reads the same bf16 rows (zero for padding tokens).
-        *reinterpret_cast<uint4*>(&out.q[i][d]) = qr;
-        *reinterpret_cast<uint4*>(&out.k[i][d]) = kr;
+        {
+            unsigned char* blk = reinterpret_cast<unsigned char*>(&out.qk[d >> 6][0][0]);
+            *reinterpret_cast<uint4*>(blk + sw128_off(i, d & 63)) = kr;
+            *reinterpret_cast<uint4*>(blk + sw128_off(DN_CHUNK + i, d & 63)) = qr;
+        }
         *reinterpret_cast<float4*>(sq + i * CL_LD + d) = make_float4(bf_lo(qr.x), bf_hi(qr.x), bf_lo(qr.y), bf_hi(qr.y));
         *reinterpret_cast<float4*>(sq + i * CL_LD + d + 4) = make_float4(bf_lo(qr.z), bf_hi(qr.z), bf_lo(qr.w), bf_hi(qr.w));
         *reinterpret_cast<float4*>(sk + i * CL_LD + d) = make_float4(bf_lo(kr.x), bf_hi(kr.x), bf_lo(kr.y), bf_hi(kr.y));
@@ -333,6 +331,15 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
         for (int i = 0; i < DN_CHUNK; ++i) { acc += sg[i]; sg[i] = acc; }
     }
     __syncthreads();
+    // k^T for the scan's state update: eight tokens of one dim are one 16-byte unit
+    for (int e = tid; e < DN_K * (DN_CHUNK / 8); e += CL_THREADS) {
+        const int d = e & (DN_K - 1), ju = e >> 7;
+        uint32_t w[4];
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj)
+            w[jj] = (__float_as_uint(sk[(ju * 8 + 2 * jj) * CL_LD + d]) >> 16) | (__float_as_uint(sk[(ju * 8 + 2 * jj + 1) * CL_LD + d]) & 0xffff0000u);
+        *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(&out.kt[0][0]) + sw128_off(d, ju * 8)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
     if (tid < DN_CHUNK) {            // the per-token factors of the scan
         const float e = expf(sg[tid]);
         se[tid] = e;
@@ -513,28 +520,34 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
 // Sequential over the chunks of a head; with S the state slice [128 k][16 v], per chunk
 //   W = w (k S),  v_new = vprime - T W,  out = d (q S) + aqk v_new,  S <- S exp(gc_last) + k^T (e v_new)
 // (w_i = beta_i exp(gc_i), d_i = exp(gc_i) / sqrt(128), e_i = exp(gc_last - gc_i); T W equals the chunk-64 formulation's
-// (T (k beta exp(gc))) S with the products taken in the other order).  All products are mma.sync tf32 tiles with the
-// accuracy of f32: q and k are bf16 values, exact as tf32 operands, so only the other operand is split hi + lo (two mma
-// per tile); T, aqk, W and v_new are split on both sides (three mma).  The eight warps form a 4 x 2 grid (16-token row tile
-// x 8-column tile):
-//   P1  warp (mt, nt): k S and q S tiles             (16 x 128 x 8 each; A fragments by ldmatrix from the bf16 rows)
-//   P1b the same warp:  T W tile -> v_new tile        (lower triangular: row tile mt sums over 16 (mt + 1) tokens)
-//   P2  the same warp:  out tile = d (q S) + aqk v_new
-//   P3  warp w: state rows 16 w .. 16 w + 15          (128 x 64 x 16; A = k^T by transposing ldmatrix)
-// Within a k-step of 8 the mma's k index t stands for element 2 t and t + 4 for element 2 t + 1, so that a bf16 pair (or a
-// float2) is one fragment pair; the B operands are read by the same rule.  The state slice lives in registers as the f32
-// accumulator fragment of P3 from chunk to chunk; shared memory holds its hi / lo split as the B operand of the next
-// chunk's P1.  The copy warp brings each chunk's operands in with three bulk copies (completion counted on an mbarrier)
-// into one of two stages, a chunk ahead of the compute warps.  Row tiles of the last chunk that hold only padding are
-// skipped.
+// (T (k beta exp(gc))) S with the products taken in the other order).  Every product has the accuracy of f32:
+//   P1  [k; q] S (128 x 128 x 16) and P3 k^T (e v_new) (128 x 64 x 16) on the 5th-generation tensor cores: tcgen05.mma
+//       kind::f16 with the bf16 rows of q and k as the left operand, exact as they are, and the f32 right operand split
+//       into three bf16 pieces (24 significant bits).  The pieces sit side by side as 48 columns of ONE right operand, so a
+//       product is 8 (P1) or 4 (P3) instructions instead of three times as many (a 16-column instruction takes as long
+//       to issue as a 48-column one); the three partial tiles are added when they are read back from tensor memory;
+//   P1b T W and P2 aqk v_new (64 x 64 x 16, lower triangular, both operands f32) as 3xTF32 mma.sync tiles, the eight warps a
+//       4 x 2 grid of (16-token row tile, 8-column tile), zero k-steps skipped.
+// The state slice lives in registers from chunk to chunk, one row (key dim) of 8 columns per thread, as it comes out of
+// tensor memory; shared memory holds its three pieces as the right operand of the next chunk's P1.  The copy warp brings
+// each chunk's operands in with three bulk copies (completion counted on an mbarrier) into one of two stages, a chunk
+// ahead of the compute warps.  Row tiles of the last chunk that hold only padding are skipped.
 constexpr int SCAN_CONS = 256;              // compute threads
 constexpr int SCAN_THREADS = SCAN_CONS + 32;
-constexpr int SCAN_LDB = SCAN_VW + 4;       // B operands (state, W, v_new; hi and lo): rows 2 t, 2 t + 1: bank = 8 t + g
+constexpr int SCAN_LDB = SCAN_VW + 4;       // W, v_new (hi and lo), d (q S): rows 2 t, 2 t + 1 of a k-step: bank = 8 t + g
 constexpr int SCAN_NSTAGE = 2;
-constexpr uint32_t SCAN_STAGE_BYTES = SCAN_QK_BYTES + SCAN_TA_BYTES + SCAN_VP_BYTES;
-constexpr int CHUNK_SCAN_SMEM = SCAN_NSTAGE * SCAN_STAGE_BYTES + (2 * DN_K + 6 * DN_CHUNK) * SCAN_LDB * 4 + 64;
-static_assert(SCAN_STAGE_BYTES % 128 == 0 || SCAN_STAGE_BYTES % 16 == 0, "stages keep 16-byte alignment");
-constexpr unsigned SCAN_WAIT_LIMIT = 1u << 26;      // a bounded wait: a copy that never lands ends the loop instead of hanging
+constexpr uint32_t SCAN_STAGE_BYTES = SCAN_QK_BYTES + SCAN_KT_BYTES + SCAN_TA_BYTES + SCAN_VP_BYTES;
+constexpr uint32_t SCAN_STAGE_PITCH = (SCAN_STAGE_BYTES + 1023u) & ~1023u;       // the swizzled blocks start on 1024-byte boundaries
+constexpr uint32_t SCAN_SP_BYTES = 2 * 3 * SCAN_VW * 128;       // state pieces:   [block of 64 dims][piece][value column][dim]
+constexpr uint32_t SCAN_VK_BYTES = 3 * SCAN_VW * 128;           // e v_new pieces: [piece][value column][token]
+constexpr int SCAN_NB = 3 * SCAN_VW;        // columns of the right operands: the three pieces side by side
+constexpr int CHUNK_SCAN_SMEM = 1024 + SCAN_NSTAGE * SCAN_STAGE_PITCH + SCAN_SP_BYTES + SCAN_VK_BYTES + 8 * DN_CHUNK * SCAN_LDB * 4 + 64;
+static_assert(CHUNK_SCAN_SMEM <= 227 * 1024, "the scan's operands must fit one CTA's shared memory");
+constexpr uint32_t SCAN_TMEM_COLS = 128;    // two 128 x 48 f32 accumulators (allocations are powers of two)
+constexpr uint32_t SCAN_D2_COL = 64;        // first column of the second accumulator
+// instruction descriptor: D f32, A / B bf16, both K-major, N = 48 at [17,23) in units of 8, M = 128 at [24,29) in units of 16
+constexpr uint32_t SCAN_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(SCAN_NB >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+constexpr unsigned SCAN_WAIT_LIMIT = 1u << 26;      // a bounded wait: a copy or an MMA that never completes ends the loop instead of hanging
 
 __device__ __forceinline__ void scan_wait(uint32_t bar, uint32_t parity, int* err) {
     unsigned it = 0;
@@ -542,7 +555,50 @@ __device__ __forceinline__ void scan_wait(uint32_t bar, uint32_t parity, int* er
         if (++it >= SCAN_WAIT_LIMIT) { atomicCAS(err, 0, (int)ERR_BARRIER_TIMEOUT); return; }
 }
 __device__ __forceinline__ void scan_cons_sync() { asm volatile("bar.sync 1, %0;" ::"n"(SCAN_CONS) : "memory"); }
-// 16 x 8 (x 16 (mt + 1)) product of a row tile of a packed lower-triangular matrix (T or aqk) with a split B operand
+// shared-memory matrix descriptor, K-major operand, 128-byte swizzle: start address >> 4 | SBO = 1024 B between 8-row groups |
+// version 1 | layout 2
+__device__ __forceinline__ uint64_t scan_smem_desc(uint32_t smem_addr) {
+    return (uint64_t)((smem_addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+__device__ __forceinline__ void scan_umma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(SCAN_IDESC), "r"(accumulate) : "memory");
+}
+__device__ __forceinline__ void scan_umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// this warp's 32 rows x 8 columns of an accumulator, one row per lane: the sum of the three partial tiles (16 columns apart),
+// small to large
+__device__ __forceinline__ void scan_tmem_ld8(uint32_t taddr, float (&v)[8]) {
+    uint32_t r[3][8];
+#pragma unroll
+    for (int pc = 0; pc < 3; ++pc)
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                     : "=r"(r[pc][0]), "=r"(r[pc][1]), "=r"(r[pc][2]), "=r"(r[pc][3]), "=r"(r[pc][4]), "=r"(r[pc][5]), "=r"(r[pc][6]), "=r"(r[pc][7])
+                     : "r"(taddr + (uint32_t)(pc * SCAN_VW)) : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = (__uint_as_float(r[2][j]) + __uint_as_float(r[1][j])) + __uint_as_float(r[0][j]);
+}
+// x = p0 + p1 + p2 up to 2^-24 |x|, each piece a bf16 value (returned as its 16 bits)
+__device__ __forceinline__ void bf16_split3(float x, unsigned short (&p)[3]) {
+    const bf16 a = __float2bfloat16_rn(x);
+    const float r1 = x - __bfloat162float(a);
+    const bf16 b = __float2bfloat16_rn(r1);
+    const bf16 c = __float2bfloat16_rn(r1 - __bfloat162float(b));
+    p[0] = __bfloat16_as_ushort(a); p[1] = __bfloat16_as_ushort(b); p[2] = __bfloat16_as_ushort(c);
+}
+// (volatile keeps these stores in order with the fences and barriers, which are volatile too; no memory clobber, so that
+// the loads around them are not serialised)
+__device__ __forceinline__ void st_shared_u16(uint32_t addr, unsigned short v) { asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v)); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// 16 x 8 (x 16 (mt + 1)) product of a row tile of a packed lower-triangular matrix (T or aqk) with a split B operand; within a
+// k-step of 8 the mma's k index t stands for column 2 t and t + 4 for column 2 t + 1, so a float2 is one fragment pair
 __device__ __forceinline__ void scan_tri_product(float (&a3)[3][4], const float* tile, int pitch, int klen, const uint32_t* bh, const uint32_t* bl,
                                                  int col, int g, int t4) {
     const float* r0 = tile + g * pitch + 2 * t4;
@@ -562,199 +618,236 @@ __device__ __forceinline__ void scan_tri_product(float (&a3)[3][4], const float*
 static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(const ChunkScratch* __restrict__ scratch, bf16* __restrict__ core_out,
                                                                         float* __restrict__ state_out, int S, int nchunks, int* __restrict__ err) {
     pdl_wait();
-    extern __shared__ __align__(128) unsigned char scan_sm[];
-    uint32_t* sth = reinterpret_cast<uint32_t*>(scan_sm + SCAN_NSTAGE * SCAN_STAGE_BYTES);     // [128][SCAN_LDB] state, tf32 hi
-    uint32_t* stl = sth + DN_K * SCAN_LDB;                                                     //                  state, tf32 lo
-    uint32_t* swh = stl + DN_K * SCAN_LDB;                                                     // [64][SCAN_LDB]  W, hi
-    uint32_t* swl = swh + DN_CHUNK * SCAN_LDB;                                                 //                  W, lo
-    uint32_t* vnh = swl + DN_CHUNK * SCAN_LDB;                                                 // [64][SCAN_LDB]  v_new, hi
-    uint32_t* vnl = vnh + DN_CHUNK * SCAN_LDB;                                                 //                  v_new, lo
-    uint32_t* vkh = vnl + DN_CHUNK * SCAN_LDB;                                                 // [64][SCAN_LDB]  e v_new, hi
-    uint32_t* vkl = vkh + DN_CHUNK * SCAN_LDB;                                                 //                  e v_new, lo
-    u64* bars = reinterpret_cast<u64*>(vkl + DN_CHUNK * SCAN_LDB);                             // full[2], empty[2]
+    extern __shared__ unsigned char scan_raw[];
+    const uint32_t raw_a = smem_u32(scan_raw), base_a = (raw_a + 1023u) & ~1023u;
+    unsigned char* sm0 = scan_raw + (base_a - raw_a);
+    const uint32_t sp_a = base_a + SCAN_NSTAGE * SCAN_STAGE_PITCH;      // state pieces
+    const uint32_t vk_a = sp_a + SCAN_SP_BYTES;                         // e v_new pieces
+    uint32_t* swh = reinterpret_cast<uint32_t*>(sm0 + SCAN_NSTAGE * SCAN_STAGE_PITCH + SCAN_SP_BYTES + SCAN_VK_BYTES);      // [64][SCAN_LDB] W, hi
+    uint32_t* swl = swh + DN_CHUNK * SCAN_LDB;                          //                 W, lo
+    uint32_t* vnh0 = swl + DN_CHUNK * SCAN_LDB;                         // [2][64][SCAN_LDB] v_new, hi   (these three by chunk parity:
+    uint32_t* vnl0 = vnh0 + 2 * DN_CHUNK * SCAN_LDB;                    //                    v_new, lo    P2 of a chunk runs during
+    float* sit0 = reinterpret_cast<float*>(vnl0 + 2 * DN_CHUNK * SCAN_LDB);   // [2][64][SCAN_LDB] d (q S)   the next chunk's P1)
+    u64* bars = reinterpret_cast<u64*>(sit0 + 2 * DN_CHUNK * SCAN_LDB);  // full[2], empty[2], P1 done, P3 done, state ready, e v_new ready
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * SCAN_NSTAGE + 4);
     const int h = blockIdx.x, vs = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t4 = lane & 3;
     const int v0 = vs * SCAN_VW;
-    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + SCAN_NSTAGE);
+    const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * SCAN_NSTAGE, p1bar = empty0 + 8 * SCAN_NSTAGE, p3bar = p1bar + 8;
+    const uint32_t sready = p3bar + 8, vkready = sready + 8;
     if (tid == 0) {
         for (int i = 0; i < SCAN_NSTAGE; ++i) {
             mbar_init(full0 + 8 * i, 1);
             mbar_init(empty0 + 8 * i, SCAN_CONS / 32);       // one arrival per compute warp
         }
+        mbar_init(p1bar, 1);
+        mbar_init(p3bar, 1);
+        mbar_init(sready, SCAN_CONS / 32);
+        mbar_init(vkready, SCAN_CONS / 32);
         mbar_fence_init();
     }
-    for (int e = tid; e < 2 * DN_K * SCAN_LDB; e += SCAN_THREADS) sth[e] = 0u;          // state = 0 (hi and lo)
+    for (uint32_t e = tid; e < SCAN_SP_BYTES / 4; e += SCAN_THREADS) reinterpret_cast<uint32_t*>(sm0 + SCAN_NSTAGE * SCAN_STAGE_PITCH)[e] = 0u;   // state = 0
+    fence_async_smem();
+    if (warp == SCAN_CONS / 32) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)), "r"(SCAN_TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
 
     if (warp == SCAN_CONS / 32) {
-        // ---- copy warp (one lane issues), one chunk ahead ----
-        if (lane == 0)
-            for (int c = 0; c < nchunks; ++c) {
+        // ---- copy and MMA warp (one lane issues both): copies run a chunk ahead; an MMA goes out as soon as its right operand
+        // is announced complete, so no compute warp waits on the issue itself ----
+        if (lane == 0) {
+            auto issue_copy = [&](int c) {
                 const ChunkScratch& in = scratch[(size_t)h * nchunks + c];
                 const int sg = c % SCAN_NSTAGE, use = c / SCAN_NSTAGE;
                 if (use > 0) scan_wait(empty0 + 8 * sg, (use - 1) & 1, err);
-                const uint32_t full = full0 + 8 * sg, dst = smem_u32(scan_sm) + sg * SCAN_STAGE_BYTES;
+                const uint32_t full = full0 + 8 * sg, dst = base_a + sg * SCAN_STAGE_PITCH;
                 mbar_arrive_expect_tx(full, SCAN_STAGE_BYTES);
-                bulk_load_1d(dst, &in.q[0][0], SCAN_QK_BYTES, full);
-                bulk_load_1d(dst + SCAN_QK_BYTES, &in.tmat[0], SCAN_TA_BYTES, full);
-                bulk_load_1d(dst + SCAN_QK_BYTES + SCAN_TA_BYTES, &in.vprime[vs][0][0], SCAN_VP_BYTES, full);
-            }
-        return;
-    }
-
-    // this warp's 16 x 16 piece of the state (rows = keys 16 warp .., columns = the slice's 16 values), f32, in registers
-    float st[2][4];
+                bulk_load_1d(dst, &in.qk[0][0][0], SCAN_QK_BYTES + SCAN_KT_BYTES, full);
+                bulk_load_1d(dst + SCAN_QK_BYTES + SCAN_KT_BYTES, &in.tmat[0], SCAN_TA_BYTES, full);
+                bulk_load_1d(dst + SCAN_QK_BYTES + SCAN_KT_BYTES + SCAN_TA_BYTES, &in.vprime[vs][0][0], SCAN_VP_BYTES, full);
+            };
+            issue_copy(0);
+            for (int c = 0; c < nchunks; ++c) {
+                const int sg = c % SCAN_NSTAGE;
+                const uint32_t qk_a = base_a + sg * SCAN_STAGE_PITCH, kt_a = qk_a + SCAN_QK_BYTES;
+                scan_wait(full0 + 8 * sg, (c / SCAN_NSTAGE) & 1, err);             // this chunk's operands have landed (long ago)
+                if (c > 0) scan_wait(sready, (c - 1) & 1, err);                    // the state's pieces after chunk c - 1
+                tc_fence_after();
+                // ---- P1: [k; q] [S0 | S1 | S2] ----
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
+                for (int kb = 0; kb < 2; ++kb) {
+                    const uint64_t adesc = scan_smem_desc(qk_a + kb * (SCAN_QK_BYTES / 2)), bdesc = scan_smem_desc(sp_a + kb * (SCAN_SP_BYTES / 2));
 #pragma unroll
-        for (int r = 0; r < 4; ++r) st[nt][r] = 0.f;
-    // the warp's tile of the 64 x 16 products: the two warps of a scheduler (warp and warp + 4) take row tiles mt and 3 - mt,
-    // whose triangular products add up to the same length
-    const int nt = warp >> 2, mt = nt ? 3 - (warp & 3) : (warp & 3), m0 = mt * 16, col = nt * 8 + g;
-    // ldmatrix row addresses (bytes from the start of q or k): P1 reads 16 rows x 16 columns, P3 16 tokens x 16 dims transposed
-    const uint32_t a_off = ((m0 + (lane & 7) + 8 * ((lane >> 3) & 1)) * SCAN_LDH + 8 * (lane >> 4)) * 2;
-    const uint32_t t_off = (((lane & 7) + 8 * (lane >> 4)) * SCAN_LDH + warp * 16 + 8 * ((lane >> 3) & 1)) * 2;
-
-    for (int c = 0; c < nchunks; ++c) {
-        const int t0 = c * DN_CHUNK;
-        const int sg = c % SCAN_NSTAGE;
-        const unsigned char* stage = scan_sm + sg * SCAN_STAGE_BYTES;
-        const uint32_t sq_a = smem_u32(stage), sk_a = sq_a + SCAN_QK_BYTES / 2;
-        const float* sT = reinterpret_cast<const float*>(stage + SCAN_QK_BYTES);
-        const float* sA = sT + SCAN_TRI;
-        const float* swsc = sA + SCAN_TRI;
-        const float* sdq = swsc + DN_CHUNK;
-        const float* skd = sdq + DN_CHUNK;
-        const float* seg = skd + DN_CHUNK;
-        const float* svp = seg + 4;
-        const int valid = min(DN_CHUNK, S - t0);
-        const bool live = mt * 16 < valid;                    // this row tile holds at least one token
-        const int kmax = (valid + 7) & ~7;                    // tokens the state update sums over, in k-steps
-        scan_wait(full0 + 8 * sg, (c / SCAN_NSTAGE) & 1, err);            // this chunk's operands have landed
-        const float dec = seg[0];
-        // ---- P1: tiles of k S and q S ----
-        float it[4] = {0.f, 0.f, 0.f, 0.f};
-        if (live) {
-            float ks2[2][2][4], it2[2][2][4];                // [half of the k range][lo / hi term]
-#pragma unroll
-            for (int i = 0; i < 16; ++i) { ks2[i >> 3][(i >> 2) & 1][i & 3] = 0.f; it2[i >> 3][(i >> 2) & 1][i & 3] = 0.f; }
-#pragma unroll 2
-            for (int c0 = 0; c0 < DN_K / 2; c0 += 16) {
-#pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-                    const int cc = c0 + hf * (DN_K / 2);
-                    uint32_t rq[4], rk[4];
-                    ldmatrix_x4(rk, sk_a + a_off + cc * 2);
-                    ldmatrix_x4(rq, sq_a + a_off + cc * 2);
-#pragma unroll
-                    for (int s2 = 0; s2 < 2; ++s2) {
-                        const uint32_t ak[4] = {rk[2 * s2] << 16, rk[2 * s2 + 1] << 16, rk[2 * s2] & 0xffff0000u, rk[2 * s2 + 1] & 0xffff0000u};
-                        const uint32_t aq[4] = {rq[2 * s2] << 16, rq[2 * s2 + 1] << 16, rq[2 * s2] & 0xffff0000u, rq[2 * s2 + 1] & 0xffff0000u};
-                        const int bi0 = (cc + 8 * s2 + 2 * t4) * SCAN_LDB + col, bi1 = bi0 + SCAN_LDB;
-                        const uint32_t bh0 = sth[bi0], bh1 = sth[bi1], bl0 = stl[bi0], bl1 = stl[bi1];
-                        mma_tf32(ks2[hf][0], ak, bl0, bl1);
-                        mma_tf32(it2[hf][0], aq, bl0, bl1);
-                        mma_tf32(ks2[hf][1], ak, bh0, bh1);
-                        mma_tf32(it2[hf][1], aq, bh0, bh1);
-                    }
+                    for (int ks = 0; ks < 4; ++ks) scan_umma(tmem_base, adesc + 2 * ks, bdesc + 2 * ks, (kb > 0 || ks > 0) ? 1u : 0u);
                 }
+                scan_umma_commit(p1bar);
+                if (c + 1 < nchunks) issue_copy(c + 1);        // its stage is released by P2 of chunk c - 1, which runs now
+                // ---- P3: k^T [e v_new 0 | 1 | 2] over the k-steps of 16 tokens that hold tokens ----
+                scan_wait(vkready, c & 1, err);
+                tc_fence_after();
+                const int nks = (min(DN_CHUNK, S - c * DN_CHUNK) + 15) >> 4;
+                const uint64_t adesc = scan_smem_desc(kt_a), bdesc = scan_smem_desc(vk_a);
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks)
+                    if (ks < nks) scan_umma(tmem_base + SCAN_D2_COL, adesc + 2 * ks, bdesc + 2 * ks, ks > 0 ? 1u : 0u);
+                scan_umma_commit(p3bar);
             }
-            // W = w (k S), split, as the B operand of P1b; d (q S) stays in registers for P2
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const int row = m0 + g + 8 * (r >> 1);
-                const float w = ((ks2[0][0][r] + ks2[1][0][r]) + (ks2[0][1][r] + ks2[1][1][r])) * swsc[row];
-                it[r] = ((it2[0][0][r] + it2[1][0][r]) + (it2[0][1][r] + it2[1][1][r])) * sdq[row];
-                uint32_t hi, lo;
-                tf32_split(w, hi, lo);
-                swh[row * SCAN_LDB + nt * 8 + 2 * t4 + (r & 1)] = hi;
-                swl[row * SCAN_LDB + nt * 8 + 2 * t4 + (r & 1)] = lo;
-            }
-        }
-        scan_cons_sync();                                              // W complete
-        // ---- P1b: v_new = vprime - T W, stored split, plain for P2 and with row i scaled by e_i for P3 ----
-        if (live) {
-            float a3[3][4];
-#pragma unroll
-            for (int i = 0; i < 12; ++i) a3[i >> 2][i & 3] = 0.f;
-            scan_tri_product(a3, sT + tri_off(mt), tri_pitch(mt), 16 * (mt + 1), swh, swl, col, g, t4);
-#pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                const int row = m0 + g + 8 * (r >> 1), cv = nt * 8 + 2 * t4 + (r & 1);
-                const float vn = svp[row * SCAN_VW + cv] - sum_terms(a3, r);
-                uint32_t hi, lo;
-                tf32_split(vn, hi, lo);
-                vnh[row * SCAN_LDB + cv] = hi;
-                vnl[row * SCAN_LDB + cv] = lo;
-                tf32_split(vn * skd[row], hi, lo);
-                vkh[row * SCAN_LDB + cv] = hi;
-                vkl[row * SCAN_LDB + cv] = lo;
-            }
-        }
-        scan_cons_sync();                                              // v_new complete
-        // ---- P2: out = d (q S) + aqk v_new ----
-        if (live) {
-            float a3[3][4];
-#pragma unroll
-            for (int i = 0; i < 12; ++i) a3[i >> 2][i & 3] = 0.f;
-            scan_tri_product(a3, sA + tri_off(mt), tri_pitch(mt), 16 * (mt + 1), vnh, vnl, col, g, t4);
-#pragma unroll
-            for (int hr = 0; hr < 2; ++hr) {
-                const int tok = t0 + m0 + g + 8 * hr;
-                if (tok < S) {
-                    bf16* dst = core_out + (size_t)tok * DN_V_SIZE + h * DN_V + v0 + nt * 8 + 2 * t4;
-                    *reinterpret_cast<__nv_bfloat162*>(dst) =
-                        __halves2bfloat162(f2bf(it[2 * hr] + sum_terms(a3, 2 * hr)), f2bf(it[2 * hr + 1] + sum_terms(a3, 2 * hr + 1)));
-                }
-            }
-        }
-        // ---- P3: S' = S exp(gc_last) + k^T (e v_new); this warp owns state rows (keys) 16 warp .. 16 warp + 15 ----
-        {
-            float a2[2][2][4];                                   // [column tile][lo / hi term]
-#pragma unroll
-            for (int i = 0; i < 16; ++i) a2[i >> 3][(i >> 2) & 1][i & 3] = 0.f;
-#pragma unroll 2
-            for (int j0 = 0; j0 < kmax; j0 += 16) {
-                uint32_t rk[4];
-                ldmatrix_x4_trans(rk, sk_a + t_off + j0 * (SCAN_LDH * 2));
-#pragma unroll
-                for (int s2 = 0; s2 < 2; ++s2) {
-                    const int jj = j0 + 8 * s2;
-                    if (jj >= kmax) continue;                        // padding tokens add nothing (uniform over the CTA)
-                    const uint32_t a[4] = {rk[2 * s2] << 16, rk[2 * s2 + 1] << 16, rk[2 * s2] & 0xffff0000u, rk[2 * s2 + 1] & 0xffff0000u};
-#pragma unroll
-                    for (int n2 = 0; n2 < 2; ++n2) {
-                        const int bi0 = (jj + 2 * t4) * SCAN_LDB + n2 * 8 + g, bi1 = bi0 + SCAN_LDB;
-                        mma_tf32(a2[n2][0], a, vkl[bi0], vkl[bi1]);
-                        mma_tf32(a2[n2][1], a, vkh[bi0], vkh[bi1]);
-                    }
-                }
-            }
-            // the new state, in registers and split for the next chunk's P1
-#pragma unroll
-            for (int n2 = 0; n2 < 2; ++n2)
-#pragma unroll
-                for (int r = 0; r < 4; ++r) {
-                    st[n2][r] = fmaf(st[n2][r], dec, a2[n2][0][r] + a2[n2][1][r]);
-                    const int row = warp * 16 + g + 8 * (r >> 1), cv = n2 * 8 + 2 * t4 + (r & 1);
-                    uint32_t hi, lo;
-                    tf32_split(st[n2][r], hi, lo);
-                    sth[row * SCAN_LDB + cv] = hi;
-                    stl[row * SCAN_LDB + cv] = lo;
-                }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(empty0 + 8 * sg, 1);                // this warp is done with the stage
-        scan_cons_sync();                                              // the new state split is complete; W and v_new may be overwritten
-    }
-    // final state in the reference layout [head][v][k], from the f32 registers
+    } else {
+        // this thread's row of the state slice: key dim 32 (warp & 3) + lane, value columns 8 (warp >> 2) .. + 7, f32
+        float st8[8];
 #pragma unroll
-    for (int n2 = 0; n2 < 2; ++n2)
+        for (int j = 0; j < 8; ++j) st8[j] = 0.f;
+        const int q4 = warp & 3, ch = warp >> 2, drow = 32 * q4 + lane;
+        const uint32_t tm_d1 = tmem_base + ((uint32_t)(32 * q4) << 16) + (uint32_t)(8 * ch), tm_d2 = tm_d1 + SCAN_D2_COL;
+        // where this row's pieces go in the right operand of P1: [dims / 64][piece][value column][dim % 64], swizzled
+        const uint32_t sp_row = sp_a + (uint32_t)(drow >> 6) * (SCAN_SP_BYTES / 2) + (uint32_t)ch * 1024u + (uint32_t)(drow & 7) * 2u;
+        // the warp's tile of the 64 x 16 mma.sync products: the two warps of a scheduler (warp and warp + 4) take row tiles mt and
+        // 3 - mt, whose triangular products add up to the same length
+        const int nt = warp >> 2, mt = nt ? 3 - (warp & 3) : (warp & 3), m0 = mt * 16, col = nt * 8 + g;
+
+        // ---- P2 of chunk cp: out = d (q S) + aqk v_new.  Not on the path to the next chunk's state, so it runs while the tensor
+        // cores work on the next chunk's P1 (after the last chunk: on its own); the chunk's stage is released after it ----
+        auto p2 = [&](int cp) {
+            const int tp = cp * DN_CHUNK, sgp = cp % SCAN_NSTAGE;
+            if (mt * 16 < S - tp) {
+                const float* sAp = reinterpret_cast<const float*>(sm0 + sgp * SCAN_STAGE_PITCH + SCAN_QK_BYTES + SCAN_KT_BYTES) + SCAN_TRI;
+                const uint32_t* vh = vnh0 + (cp & 1) * DN_CHUNK * SCAN_LDB;
+                const uint32_t* vl = vnl0 + (cp & 1) * DN_CHUNK * SCAN_LDB;
+                const float* si = sit0 + (cp & 1) * DN_CHUNK * SCAN_LDB;
+                float a3[3][4];
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-            const int d = warp * 16 + g + 8 * (r >> 1), v = n2 * 8 + 2 * t4 + (r & 1);
-            state_out[((size_t)h * DN_V + v0 + v) * DN_K + d] = st[n2][r];
+                for (int i = 0; i < 12; ++i) a3[i >> 2][i & 3] = 0.f;
+                scan_tri_product(a3, sAp + tri_off(mt), tri_pitch(mt), 16 * (mt + 1), vh, vl, col, g, t4);
+#pragma unroll
+                for (int hr = 0; hr < 2; ++hr) {
+                    const int row = m0 + g + 8 * hr, tok = tp + row;
+                    if (tok < S) {
+                        const float2 it = *reinterpret_cast<const float2*>(si + row * SCAN_LDB + nt * 8 + 2 * t4);
+                        bf16* dst = core_out + (size_t)tok * DN_V_SIZE + h * DN_V + v0 + nt * 8 + 2 * t4;
+                        *reinterpret_cast<__nv_bfloat162*>(dst) =
+                            __halves2bfloat162(f2bf(it.x + sum_terms(a3, 2 * hr)), f2bf(it.y + sum_terms(a3, 2 * hr + 1)));
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty0 + 8 * sgp, 1);               // this warp is done with the stage
+        };
+
+        for (int c = 0; c < nchunks; ++c) {
+            const int t0 = c * DN_CHUNK;
+            const int sg = c % SCAN_NSTAGE;
+            const float* sT = reinterpret_cast<const float*>(sm0 + sg * SCAN_STAGE_PITCH + SCAN_QK_BYTES + SCAN_KT_BYTES);
+            const float* sA = sT + SCAN_TRI;
+            const float* swsc = sA + SCAN_TRI;
+            const float* sdq = swsc + DN_CHUNK;
+            const float* skd = sdq + DN_CHUNK;
+            const float* seg = skd + DN_CHUNK;
+            const float* svp = seg + 4;
+            const int valid = min(DN_CHUNK, S - t0);
+            const bool live = mt * 16 < valid;                    // this row tile holds at least one token
+            uint32_t* vnh = vnh0 + (c & 1) * DN_CHUNK * SCAN_LDB;
+            uint32_t* vnl = vnl0 + (c & 1) * DN_CHUNK * SCAN_LDB;
+            float* sit = sit0 + (c & 1) * DN_CHUNK * SCAN_LDB;
+            scan_wait(full0 + 8 * sg, (c / SCAN_NSTAGE) & 1, err);            // this chunk's operands have landed
+            const float dec = seg[0];
+            if (c > 0) p2(c - 1);
+            scan_wait(p1bar, c & 1, err);
+            __syncwarp();
+            tc_fence_after();
+            {
+                float v[8];
+                scan_tmem_ld8(tm_d1, v);
+                if (q4 < 2) {            // rows of k S: W = w (k S), split, as the B operand of P1b
+                    const float w = swsc[drow];
+                    uint32_t hi[8], lo[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) tf32_split(v[j] * w, hi[j], lo[j]);
+                    uint4* dh = reinterpret_cast<uint4*>(swh + drow * SCAN_LDB + 8 * ch);
+                    uint4* dl = reinterpret_cast<uint4*>(swl + drow * SCAN_LDB + 8 * ch);
+                    dh[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]); dh[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+                    dl[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]); dl[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+                } else {                 // rows of q S: d (q S), for P2
+                    const float d = sdq[drow - DN_CHUNK];
+                    float4* di = reinterpret_cast<float4*>(sit + (drow - DN_CHUNK) * SCAN_LDB + 8 * ch);
+                    di[0] = make_float4(v[0] * d, v[1] * d, v[2] * d, v[3] * d);
+                    di[1] = make_float4(v[4] * d, v[5] * d, v[6] * d, v[7] * d);
+                }
+            }
+            tc_fence_before();
+            scan_cons_sync();                                              // W and d (q S) complete
+            // ---- P1b: v_new = vprime - T W, stored split for P2 and, with row i scaled by e_i, in three bf16 pieces for P3 ----
+            if (live) {
+                float a3[3][4];
+#pragma unroll
+                for (int i = 0; i < 12; ++i) a3[i >> 2][i & 3] = 0.f;
+                scan_tri_product(a3, sT + tri_off(mt), tri_pitch(mt), 16 * (mt + 1), swh, swl, col, g, t4);
+                float vpv[4], kdv[2];
+#pragma unroll
+                for (int r = 0; r < 4; ++r) vpv[r] = svp[(m0 + g + 8 * (r >> 1)) * SCAN_VW + nt * 8 + 2 * t4 + (r & 1)];
+                kdv[0] = skd[m0 + g];
+                kdv[1] = skd[m0 + g + 8];
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const int row = m0 + g + 8 * (r >> 1), cv = nt * 8 + 2 * t4 + (r & 1);
+                    const float vn = vpv[r] - sum_terms(a3, r);
+                    uint32_t hi, lo;
+                    tf32_split(vn, hi, lo);
+                    vnh[row * SCAN_LDB + cv] = hi;
+                    vnl[row * SCAN_LDB + cv] = lo;
+                    unsigned short pcs[3];
+                    bf16_split3(vn * kdv[r >> 1], pcs);
+                    const uint32_t a = vk_a + (uint32_t)nt * 1024u + (uint32_t)(cv & 7) * 128u + ((uint32_t)((row >> 3) ^ (cv & 7)) << 4) + (uint32_t)(row & 7) * 2u;
+                    st_shared_u16(a, pcs[0]);
+                    st_shared_u16(a + 2048, pcs[1]);
+                    st_shared_u16(a + 4096, pcs[2]);
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(vkready, 1);                        // this warp's part of the right operand of P3 is written
+            scan_cons_sync();                                              // v_new complete (P2 reads it in the next iteration)
+            // ---- the new state: S exp(gc_last) + P3, in registers and in pieces for the next chunk's P1 ----
+            scan_wait(p3bar, c & 1, err);
+            __syncwarp();
+            tc_fence_after();
+            {
+                float v[8];
+                scan_tmem_ld8(tm_d2, v);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    st8[j] = fmaf(st8[j], dec, v[j]);
+                    unsigned short pcs[3];
+                    bf16_split3(st8[j], pcs);
+                    const uint32_t a = sp_row + (uint32_t)j * 128u + ((uint32_t)(((drow & 63) >> 3) ^ j) << 4);
+                    st_shared_u16(a, pcs[0]);
+                    st_shared_u16(a + 2048, pcs[1]);
+                    st_shared_u16(a + 4096, pcs[2]);
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(sready, 1);                         // this warp's rows of the next P1's right operand are written
         }
+        p2(nchunks - 1);
+        // final state in the reference layout [head][v][k], from the f32 registers
+#pragma unroll
+        for (int j = 0; j < 8; ++j) state_out[((size_t)h * DN_V + v0 + 8 * ch + j) * DN_K + drow] = st8[j];
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == SCAN_CONS / 32) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(SCAN_TMEM_COLS) : "memory");
+    }
 }
 
 // ---- gated RMSNorm of the DeltaNet output: one warp per (token, head) --------------------------------
