@@ -349,6 +349,7 @@ def run_ours(args):
     if args.tree_verify and rank == 0:
         tree = tree_verify_bench(dev)
         tree["q8_0_kv_cache_ms"] = tree_verify_bench(dev, iters=3, kv_type="q8_0")["ms_per_verify_commit"]
+        tree["q4_0_kv_cache_ms"] = tree_verify_bench(dev, iters=3, kv_type="q4_0")["ms_per_verify_commit"]
         torch.cuda.empty_cache()
         draft = draft_forward_bench(dev)
     if world > 1:

@@ -294,7 +294,7 @@ typedef struct {
     const int* node_tokens;          /* device int32 [n_nodes] */
     const int* parents;              /* device int32 [n_nodes] */
     int past; int max_ctx;           /* committed tokens; cache capacity (past + n_nodes <= max_ctx) */
-    void* k_cache; void* v_cache;    /* bf16 [n_fa][kv_heads][max_ctx][256] (or Q8_0 rows, see kv_type); node t is written at slot past + t */
+    void* k_cache; void* v_cache;    /* bf16 [n_fa][kv_heads][max_ctx][256] (or rows of another type, see kv_type); node t is written at slot past + t */
     void* ssm_state;                 /* f32 [n_dn][v_heads][128 value][128 key] */
     void* conv_state;                /* f32 [n_dn][3][conv_ch], row 2 newest */
     void* node_states;               /* f16 [n_dn][max_nodes][v_heads][128][128]: every node's post-state */
@@ -313,9 +313,11 @@ typedef struct {
     int feat_cap;                    /* ring capacity in positions */
     int n_capture;                   /* 0..8 captured layers */
     int capture_layers[8];           /* layer indices, ascending (the reference's target: 1, 16, 31, 46, 61) */
-    /* 0: k_cache / v_cache rows are bf16 [256].  1: Q8_0, the reference's default cache type
-     * (qwen35_target_graph.cpp:110-122): rows of 8 blocks {f16 d, 32 x int8} = 272 bytes, caches
-     * uint8 [n_fa][kv_heads][max_ctx][272]; a row is quantised from its f32 values when written and read as bf16(d*q). */
+    /* 0: k_cache / v_cache rows are bf16 [256].  The reference's cache types (qwen35_target_graph.cpp:110-122):
+     * 1: Q8_0, its default: rows of 8 blocks {f16 d, 32 x int8} = 272 bytes, caches uint8 [n_fa][kv_heads][max_ctx][272];
+     * 2: Q4_0: rows of 8 blocks {f16 d, 16 bytes of 4-bit codes} = 144 bytes, caches uint8 [..][144];
+     * 3: F16 rows [256].
+     * A row is converted from its f32 values when written and read as the bf16 operand bf16(value). */
     int kv_type;
 } Qwen35TreeVerifyArgs;
 

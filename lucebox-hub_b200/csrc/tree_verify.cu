@@ -147,12 +147,20 @@ __global__ void tv_tree_prep_kernel(const int* __restrict__ parents, int n, int*
     }
 }
 
-// K / V cache rows: bf16 [256] (512 bytes), or Q8_0 (the reference's default cache type, qwen35_target_graph.cpp:110-122):
-// 8 blocks of {f16 d, 32 x int8} = 272 bytes, quantised from the f32 values when a row is written
-// (d = amax / 127, q = roundf(x / d)) and read back as the bf16 operand bf16(d * q).
+// K / V cache rows, by kv_type (the reference's cache types, qwen35_target_graph.cpp:110-122, plus this library's bf16):
+//   0 bf16 [256] (512 bytes);
+//   1 Q8_0 (the reference's default): 8 blocks of {f16 d, 32 x int8} = 272 bytes, d = amax / 127, q = roundf(x / d);
+//   2 Q4_0: 8 blocks of {f16 d, 16 bytes of nibbles} = 144 bytes, d = (the element of largest magnitude) / -8,
+//     q = min(15, trunc(x / d + 8.5)), byte j = q[j] | q[j + 16] << 4, value d (q - 8);
+//   3 F16 [256] (512 bytes).
+// Quantised from the f32 values when a row is written and read back as the bf16 operand bf16(value).
+constexpr int TV_KV_BF16 = 0, TV_KV_Q8_0 = 1, TV_KV_Q4_0 = 2, TV_KV_F16 = 3;
 constexpr int TV_Q8_ROW = (TV_HD / 32) * 34;
+constexpr int TV_Q4_ROW = (TV_HD / 32) * 18;
 constexpr int TV_PV_THREADS = 512;      // scores and P.V kernels: 16 warps share a chunk (latency-bound with 8; P.V: 99 exp + divide per thread)
-__host__ __device__ constexpr int tv_kv_row_bytes(int kv_type) { return kv_type ? TV_Q8_ROW : TV_HD * 2; }
+__host__ __device__ constexpr int tv_kv_row_bytes(int kv_type) { return kv_type == TV_KV_Q8_0 ? TV_Q8_ROW : kv_type == TV_KV_Q4_0 ? TV_Q4_ROW : TV_HD * 2; }
+// bytes of the raw staging buffer the attention kernels need beside the bf16 tile (the 512-byte row types land in the tile)
+__host__ __device__ constexpr int tv_kv_raw_bytes(int kv_type) { return kv_type == TV_KV_Q8_0 ? TV_CHUNK * TV_Q8_ROW : kv_type == TV_KV_Q4_0 ? TV_CHUNK * TV_Q4_ROW : 0; }
 
 // one warp = one 32-element block: lane holds element `lane` of the block
 __device__ __forceinline__ void tv_q8_store_block(unsigned char* blk, float v, int lane) {
@@ -162,15 +170,51 @@ __device__ __forceinline__ void tv_q8_store_block(unsigned char* blk, float v, i
     blk[2 + lane] = (unsigned char)(signed char)(int)roundf(v * id);
     if (lane == 0) *reinterpret_cast<__half*>(blk) = __float2half_rn(d);
 }
+__device__ __forceinline__ void tv_q4_store_block(unsigned char* blk, float v, int lane) {
+    // the element of largest magnitude, the first one among equals, with its sign
+    float best = fabsf(v);
+    int bi = lane;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    const float mx = __shfl_sync(0xffffffffu, v, bi);
+    const float d = mx * -0.125f;
+    const float id = d != 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+    const int q = min(15, (int)__fadd_rn(__fmul_rn(v, id), 8.5f));        // >= 0.5 before truncation; no fused multiply-add
+    const int hi = __shfl_down_sync(0xffffffffu, q, 16);
+    if (lane < 16) blk[2 + lane] = (unsigned char)(q | (hi << 4));
+    if (lane == 0) *reinterpret_cast<__half*>(blk) = __float2half_rn(d);
+}
+// 128 threads write one cache row from its 256 f32 values: thread tid holds elements tid and tid + 128
+__device__ __forceinline__ void tv_store_kv_row(unsigned char* row, float a, float b, int tid, int kv_type) {
+    if (kv_type == TV_KV_Q8_0) {                                   // warp w holds blocks w and 4 + w
+        tv_q8_store_block(row + (tid >> 5) * 34, a, tid & 31);
+        tv_q8_store_block(row + (4 + (tid >> 5)) * 34, b, tid & 31);
+    } else if (kv_type == TV_KV_Q4_0) {
+        tv_q4_store_block(row + (tid >> 5) * 18, a, tid & 31);
+        tv_q4_store_block(row + (4 + (tid >> 5)) * 18, b, tid & 31);
+    } else if (kv_type == TV_KV_F16) {
+        __half* dst = reinterpret_cast<__half*>(row);
+        dst[tid] = __float2half_rn(a); dst[tid + 128] = __float2half_rn(b);
+    } else {
+        bf16* dst = reinterpret_cast<bf16*>(row);
+        dst[tid] = f2bf(a); dst[tid + 128] = f2bf(b);
+    }
+}
 
-// stage 128 cache rows [j0, j0 + 128) of one kv head into the padded bf16 tile; rows >= L are zero.  bf16 rows are copied
-// straight into the tile; Q8_0 rows are copied raw into `raw` and converted by tv_finish_rows after the copies landed.
-template <bool Q8>
+// stage 128 cache rows [j0, j0 + 128) of one kv head into the padded bf16 tile; rows >= L are zero.  512-byte rows are copied
+// straight into the tile (F16 rows are converted in place afterwards); Q8_0 and Q4_0 rows are copied raw into `raw`;
+// tv_finish_rows converts after the copies landed.
+template <int KT>
 __device__ __forceinline__ void tv_stage_rows(bf16* tile, unsigned char* raw, const unsigned char* head_base, int j0, int L, int tid, int nthr = 256) {
-    if (Q8) {
-        for (int i = tid; i < TV_CHUNK * (TV_Q8_ROW / 16); i += nthr) {
-            const int k = i / (TV_Q8_ROW / 16), c = i % (TV_Q8_ROW / 16);
-            if (j0 + k < L) cp_async16(raw + (size_t)k * TV_Q8_ROW + c * 16, head_base + (size_t)(j0 + k) * TV_Q8_ROW + c * 16);
+    if (KT == TV_KV_Q8_0 || KT == TV_KV_Q4_0) {
+        constexpr int ROW = tv_kv_row_bytes(KT);
+        for (int i = tid; i < TV_CHUNK * (ROW / 16); i += nthr) {
+            const int k = i / (ROW / 16), c = i % (ROW / 16);
+            if (j0 + k < L) cp_async16(raw + (size_t)k * ROW + c * 16, head_base + (size_t)(j0 + k) * ROW + c * 16);
         }
     } else {
         for (int i = tid; i < TV_CHUNK * (TV_HD / 8); i += nthr) {
@@ -181,14 +225,36 @@ __device__ __forceinline__ void tv_stage_rows(bf16* tile, unsigned char* raw, co
         }
     }
 }
-// call after cp_async_wait_all() + __syncthreads(); for Q8_0 converts the raw rows and synchronises again
-template <bool Q8>
+// call after cp_async_wait_all() + __syncthreads(); converts the rows of the other types to bf16 and synchronises again
+template <int KT>
 __device__ __forceinline__ void tv_finish_rows(bf16* tile, const unsigned char* raw, int j0, int L, int tid, int nthr = 256) {
-    if (!Q8) return;
+    if (KT == TV_KV_BF16) return;
+    if (KT == TV_KV_F16) {
+        for (int i = tid; i < TV_CHUNK * (TV_HD / 8); i += nthr) {
+            const int k = i / (TV_HD / 8), c8 = i % (TV_HD / 8);
+            if (j0 + k >= L) continue;                                    // zero rows stay zero
+            uint4* p = reinterpret_cast<uint4*>(tile + (size_t)k * TV_QSTRIDE + c8 * 8);
+            const uint4 h = *p;
+            const uint32_t in[4] = {h.x, h.y, h.z, h.w};
+            uint32_t o[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&in[e]));
+                const __nv_bfloat162 pr = __floats2bfloat162_rn(f.x, f.y);
+                o[e] = *reinterpret_cast<const uint32_t*>(&pr);
+            }
+            *p = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        __syncthreads();
+        return;
+    }
     for (int i = tid; i < TV_CHUNK * (TV_HD / 32); i += nthr) {
         const int k = i / (TV_HD / 32), b = i % (TV_HD / 32);
         uint32_t o[16];
-        if (j0 + k < L) {
+        if (j0 + k >= L) {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) o[e] = 0u;
+        } else if (KT == TV_KV_Q8_0) {
             const unsigned char* blk = raw + (size_t)k * TV_Q8_ROW + b * 34;
             const float d = __half2float(*reinterpret_cast<const __half*>(blk));
 #pragma unroll
@@ -198,8 +264,18 @@ __device__ __forceinline__ void tv_finish_rows(bf16* tile, const unsigned char* 
                 o[e] = *reinterpret_cast<const uint32_t*>(&pr);
             }
         } else {
+            // Q4_0: byte j holds elements j (low nibble) and j + 16 (high nibble); output pair e = elements 2 e, 2 e + 1
+            const unsigned char* blk = raw + (size_t)k * TV_Q4_ROW + b * 18;
+            const float d = __half2float(*reinterpret_cast<const __half*>(blk));
 #pragma unroll
-            for (int e = 0; e < 16; ++e) o[e] = 0u;
+            for (int e = 0; e < 8; ++e) {
+                const unsigned short two = *reinterpret_cast<const unsigned short*>(blk + 2 + 2 * e);     // bytes 2 e, 2 e + 1
+                const int b0 = two & 0xFF, b1 = two >> 8;
+                const __nv_bfloat162 lo = __floats2bfloat162_rn(d * (float)((b0 & 15) - 8), d * (float)((b1 & 15) - 8));
+                const __nv_bfloat162 hi = __floats2bfloat162_rn(d * (float)((b0 >> 4) - 8), d * (float)((b1 >> 4) - 8));
+                o[e] = *reinterpret_cast<const uint32_t*>(&lo);
+                o[8 + e] = *reinterpret_cast<const uint32_t*>(&hi);
+            }
         }
         uint4* dst = reinterpret_cast<uint4*>(tile + (size_t)k * TV_QSTRIDE + b * 32);
 #pragma unroll
@@ -224,13 +300,7 @@ __global__ void __launch_bounds__(128) tv_fa_prep_kernel(const bf16* __restrict_
         const int kvh = slot - D.q_heads - D.kv_heads;
         const bf16* src = row + qcols + (D.kv_heads + kvh) * TV_HD;
         unsigned char* vrow = v_cache + ((size_t)kvh * max_ctx + past + t) * tv_kv_row_bytes(kv_type);
-        if (kv_type) {                                             // warp w holds blocks w and 4 + w
-            tv_q8_store_block(vrow + (tid >> 5) * 34, bf2f(src[tid]), tid & 31);
-            tv_q8_store_block(vrow + (4 + (tid >> 5)) * 34, bf2f(src[tid + 128]), tid & 31);
-        } else {
-            bf16* dst = reinterpret_cast<bf16*>(vrow);
-            dst[tid] = src[tid]; dst[tid + 128] = src[tid + 128];
-        }
+        tv_store_kv_row(vrow, bf2f(src[tid]), bf2f(src[tid + 128]), tid, kv_type);
         return;
     }
     const bool isq = slot < D.q_heads;
@@ -257,20 +327,17 @@ __global__ void __launch_bounds__(128) tv_fa_prep_kernel(const bf16* __restrict_
         }
         y[k] = v;
     }
-    if (!isq && kv_type) {
-        unsigned char* krow = k_cache + ((size_t)(slot - D.q_heads) * max_ctx + past + t) * TV_Q8_ROW;
-        tv_q8_store_block(krow + (tid >> 5) * 34, y[0], tid & 31);
-        tv_q8_store_block(krow + (4 + (tid >> 5)) * 34, y[1], tid & 31);
+    if (!isq) {
+        tv_store_kv_row(k_cache + ((size_t)(slot - D.q_heads) * max_ctx + past + t) * tv_kv_row_bytes(kv_type), y[0], y[1], tid, kv_type);
         return;
     }
-    bf16* dst = isq ? qbuf + ((size_t)t * D.q_heads + slot) * TV_HD
-                    : reinterpret_cast<bf16*>(k_cache + ((size_t)(slot - D.q_heads) * max_ctx + past + t) * TV_HD * 2);
+    bf16* dst = qbuf + ((size_t)t * D.q_heads + slot) * TV_HD;
     dst[tid] = f2bf(y[0]); dst[tid + 128] = f2bf(y[1]);
 }
 
 // scores of all query rows of one kv head (row r = node * gqa + q-in-group) against one chunk of keys:
 // s = (q . k) / 16 in f32, masked to -inf outside [0, past) and the node's ancestors.  grid (chunks, kv_heads).
-template <bool Q8>
+template <int KT>
 __global__ void __launch_bounds__(TV_PV_THREADS, 1) tv_att_scores_kernel(const bf16* __restrict__ qbuf, const unsigned char* __restrict__ k_cache,
                                                                const unsigned long long* __restrict__ anc, TvDims D, int n_nodes, int past,
                                                                int max_ctx, int lpad, float* __restrict__ scores) {
@@ -288,11 +355,11 @@ __global__ void __launch_bounds__(TV_PV_THREADS, 1) tv_att_scores_kernel(const b
         if (r < R) cp_async16(dst, qbuf + ((size_t)(r / gqa) * D.q_heads + kvh * gqa + r % gqa) * TV_HD + c8 * 8);
         else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
     }
-    unsigned char* raw = reinterpret_cast<unsigned char*>(Ks + (size_t)TV_CHUNK * TV_QSTRIDE);      // Q8_0 only
-    tv_stage_rows<Q8>(Ks, raw, k_cache + (size_t)kvh * max_ctx * tv_kv_row_bytes(Q8), j0, L, tid, TV_PV_THREADS);
+    unsigned char* raw = reinterpret_cast<unsigned char*>(Ks + (size_t)TV_CHUNK * TV_QSTRIDE);      // the quantised types only
+    tv_stage_rows<KT>(Ks, raw, k_cache + (size_t)kvh * max_ctx * tv_kv_row_bytes(KT), j0, L, tid, TV_PV_THREADS);
     cp_async_wait_all();
     __syncthreads();
-    tv_finish_rows<Q8>(Ks, raw, j0, L, tid, TV_PV_THREADS);
+    tv_finish_rows<KT>(Ks, raw, j0, L, tid, TV_PV_THREADS);
     const int g = lane >> 2, c = lane & 3;
     // 16 warps: warp w owns the 16 keys [16 kp, 16 kp + 16), kp = w mod 8, of the chunk = two 8-key MMA tiles (their K
     // fragments, by ldmatrix, stay in registers for the whole kernel) and every other pair of query tiles (w / 8).  Query
@@ -368,7 +435,7 @@ __global__ void __launch_bounds__(256) tv_att_stats_kernel(const float* __restri
 // partial P.V of one chunk of keys for all query rows of one kv head; P = bf16(exp(s - m) / l).  grid (chunks, kv_heads).
 // The V chunk is staged row-major by cp.async and read as the B operand with ldmatrix.trans; P goes to shared memory
 // row-major and is read as the A operand with ldmatrix.
-template <bool Q8>
+template <int KT>
 __global__ void __launch_bounds__(TV_PV_THREADS, 1) tv_att_pv_kernel(const unsigned char* __restrict__ v_cache, const float* __restrict__ scores, const float* __restrict__ stats,
                                                            TvDims D, int n_nodes, int past, int max_ctx, int lpad, float* __restrict__ partial) {
     pdl_wait();
@@ -378,8 +445,8 @@ __global__ void __launch_bounds__(TV_PV_THREADS, 1) tv_att_pv_kernel(const unsig
     const int gqa = D.q_heads / D.kv_heads, R = n_nodes * gqa, mt_n = (R + 15) / 16;
     const int chunk = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int j0 = chunk * TV_CHUNK, L = past + n_nodes;
-    unsigned char* raw = reinterpret_cast<unsigned char*>(Ps + (size_t)mt_n * 16 * TV_PSTRIDE);      // Q8_0 only
-    tv_stage_rows<Q8>(Vs, raw, v_cache + (size_t)kvh * max_ctx * tv_kv_row_bytes(Q8), j0, L, tid, TV_PV_THREADS);
+    unsigned char* raw = reinterpret_cast<unsigned char*>(Ps + (size_t)mt_n * 16 * TV_PSTRIDE);      // the quantised types only
+    tv_stage_rows<KT>(Vs, raw, v_cache + (size_t)kvh * max_ctx * tv_kv_row_bytes(KT), j0, L, tid, TV_PV_THREADS);
     // P rows (overlapping the copies above): a warp takes one row at a time, a lane four consecutive keys, so the score
     // loads are 16-byte, coalesced and several rows deep in flight
     static_assert(TV_CHUNK == 128, "one warp covers a 128-key row with four keys per lane");
@@ -399,7 +466,7 @@ __global__ void __launch_bounds__(TV_PV_THREADS, 1) tv_att_pv_kernel(const unsig
     }
     cp_async_wait_all();
     __syncthreads();
-    tv_finish_rows<Q8>(Vs, raw, j0, L, tid, TV_PV_THREADS);
+    tv_finish_rows<KT>(Vs, raw, j0, L, tid, TV_PV_THREADS);
     const int g = lane >> 2, c = lane & 3;
     const int n_chunks = gridDim.x;
     for (int np = warp; np < TV_HD / 16; np += TV_PV_THREADS / 32) {                   // pairs of 8-dim output tiles
@@ -841,10 +908,11 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
     const size_t pv_smem = ((size_t)TV_CHUNK * TV_QSTRIDE + (size_t)mt_n * 16 * TV_PSTRIDE) * 2;
     static PerDeviceOnce attr_done;
     if (attr_done.pending()) {
-        Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_scores_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-        Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_scores_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-        Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_pv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-        Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_pv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+#define TV_ATT_SMEM(KT)                                                                                                           \
+        Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_scores_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)); \
+        Q35_CUDA_OK(cudaFuncSetAttribute(tv_att_pv_kernel<KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+        TV_ATT_SMEM(TV_KV_BF16) TV_ATT_SMEM(TV_KV_Q8_0) TV_ATT_SMEM(TV_KV_Q4_0) TV_ATT_SMEM(TV_KV_F16)
+#undef TV_ATT_SMEM
         Q35_CUDA_OK(cudaFuncSetAttribute(tv_dn_tree_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tv_dn_tree_smem(TV_MAX_NODES)));
         attr_done.mark();
     }
@@ -858,9 +926,9 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
         Q35_CUDA_OK(cudaEventCreateWithFlags(&side.fork, cudaEventDisableTiming));
         Q35_CUDA_OK(cudaEventCreateWithFlags(&side.join, cudaEventDisableTiming));
     }
-    const bool q8 = in->kv_type != 0;
+    if (in->kv_type < 0 || in->kv_type > TV_KV_F16) { set_error("tree_verify: kv_type %d (0 bf16, 1 Q8_0, 2 Q4_0, 3 F16)", in->kv_type); return QWEN35_ERR_BAD_ARG; }
     const size_t kv_layer = (size_t)D.kv_heads * in->max_ctx * tv_kv_row_bytes(in->kv_type);      // bytes
-    const size_t q8_raw = q8 ? (size_t)TV_CHUNK * TV_Q8_ROW : 0;
+    const size_t kv_raw = (size_t)tv_kv_raw_bytes(in->kv_type);
     const size_t state_layer = (size_t)D.dn_v_heads * TV_DN * TV_DN;
     const size_t nstate_layer = (size_t)in->max_nodes * state_layer, nconv_layer = (size_t)in->max_nodes * conv_ch;
     if (in->max_nodes < n) { set_error("tree_verify: max_nodes %d < n_nodes %d", in->max_nodes, n); return QWEN35_ERR_BAD_ARG; }
@@ -891,11 +959,17 @@ extern "C" int qwen35_b200_tree_verify(const Qwen35TreeVerifyArgs* in, qwen35_st
             unsigned char* vc = (unsigned char*)in->v_cache + (size_t)i_fa * kv_layer;
             Q35_CUDA_OK(pdl_launch(tv_fa_prep_kernel, dim3(n, D.q_heads + 2 * D.kv_heads), 128, 0, stream, s.proj, fa_in, (const float*)W.q_norm, (const float*)W.k_norm, s.depth, D,
                                                                                        in->past, in->max_ctx, s.qbuf, kc, vc, in->kv_type));
-            if (q8) Q35_CUDA_OK(pdl_launch(tv_att_scores_kernel<true>, dim3(chunks, D.kv_heads), TV_PV_THREADS, sc_smem + q8_raw, stream, s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores));
-            else Q35_CUDA_OK(pdl_launch(tv_att_scores_kernel<false>, dim3(chunks, D.kv_heads), TV_PV_THREADS, sc_smem, stream, s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores));
+            switch (in->kv_type) {
+#define TV_SCORES(KT) case KT: Q35_CUDA_OK(pdl_launch(tv_att_scores_kernel<KT>, dim3(chunks, D.kv_heads), TV_PV_THREADS, sc_smem + kv_raw, stream, s.qbuf, kc, s.anc, D, n, in->past, in->max_ctx, lpad, s.scores)); break;
+                TV_SCORES(TV_KV_BF16) TV_SCORES(TV_KV_Q8_0) TV_SCORES(TV_KV_Q4_0) TV_SCORES(TV_KV_F16)
+#undef TV_SCORES
+            }
             Q35_CUDA_OK(pdl_launch(tv_att_stats_kernel, (D.kv_heads * R + 7) / 8, 256, 0, stream, s.scores, D.kv_heads * R, lpad, chunks * TV_CHUNK, s.stats));
-            if (q8) Q35_CUDA_OK(pdl_launch(tv_att_pv_kernel<true>, dim3(chunks, D.kv_heads), TV_PV_THREADS, pv_smem + q8_raw, stream, vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial));
-            else Q35_CUDA_OK(pdl_launch(tv_att_pv_kernel<false>, dim3(chunks, D.kv_heads), TV_PV_THREADS, pv_smem, stream, vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial));
+            switch (in->kv_type) {
+#define TV_PV(KT) case KT: Q35_CUDA_OK(pdl_launch(tv_att_pv_kernel<KT>, dim3(chunks, D.kv_heads), TV_PV_THREADS, pv_smem + kv_raw, stream, vc, s.scores, s.stats, D, n, in->past, in->max_ctx, lpad, s.partial)); break;
+                TV_PV(TV_KV_BF16) TV_PV(TV_KV_Q8_0) TV_PV(TV_KV_Q4_0) TV_PV(TV_KV_F16)
+#undef TV_PV
+            }
             Q35_CUDA_OK(pdl_launch(tv_att_merge_kernel, dim3(n, D.q_heads), 128, 0, stream, s.partial, s.proj, fa_in, D, n, chunks, s.attn));
             g_launches.fetch_add(5);
             att_w = D.q_heads * TV_HD;

@@ -123,13 +123,18 @@ def random_tree(n_nodes, max_depth, seed):
     return parents
 
 
+KV_TYPES = {"bf16": 0, "q8_0": 1, "q4_0": 2, "f16": 3}       # the library's kv_type codes
+KV_BLOCK_BYTES = {"q8_0": 34, "q4_0": 18}                    # bytes per 32-element block of the quantised types
+
+
 class TreeTarget:
     """Caches, weights table and scratch of one target model instance on one GPU."""
 
     def __init__(self, dims: TreeDims, weights, max_ctx: int, device="cuda", max_nodes: int = MAX_NODES, capture_layers=(), feat_cap: int = 0,
                  kv_type: str = "bf16"):
-        """kv_type: "bf16" or "q8_0" (the reference's default K / V cache type): Q8_0 caches are uint8
-        [n_fa, kv_heads, max_ctx, 272], rows quantised in the kernel when a node is written.
+        """kv_type: "bf16", or one of the reference's K / V cache types (qwen35_target_graph.cpp:110-122): "q8_0" (its
+        default; uint8 [n_fa, kv_heads, max_ctx, 272]), "q4_0" (uint8 [..., 144]) or "f16"; rows are converted in the
+        kernel when a node is written and read back as bf16 operands.
         capture_layers / feat_cap: keep the outputs of those layers in a ring of feat_cap positions for the draft
         (`target_feat`, bf16 [feat_cap, len(capture_layers) * hidden]; the reference's target captures layers 1, 16, 31, 46, 61)."""
         self.dims, self.max_ctx, self.max_nodes = dims, int(max_ctx), int(max_nodes)
@@ -153,13 +158,14 @@ class TreeTarget:
             self._layers_c[il].dense_mask = mask
         self._dense_mask = (1 if weights["token_embd"].dtype == torch.bfloat16 else 0) | (2 if weights["output_w"].dtype == torch.bfloat16 else 0)
         dev = self.device
-        if kv_type not in ("bf16", "q8_0"):
-            raise ValueError("kv_type must be 'bf16' or 'q8_0'")
+        if kv_type not in KV_TYPES:
+            raise ValueError("kv_type must be one of %s" % (sorted(KV_TYPES),))
         self.kv_type = kv_type
-        if kv_type == "q8_0":
-            self.k_cache = torch.zeros(max(D.n_fa, 1), D.kv_heads, self.max_ctx, D.head_dim // 32 * 34, dtype=torch.uint8, device=dev)
+        if kv_type in KV_BLOCK_BYTES:
+            self.k_cache = torch.zeros(max(D.n_fa, 1), D.kv_heads, self.max_ctx, D.head_dim // 32 * KV_BLOCK_BYTES[kv_type], dtype=torch.uint8, device=dev)
         else:
-            self.k_cache = torch.zeros(max(D.n_fa, 1), D.kv_heads, self.max_ctx, D.head_dim, dtype=torch.bfloat16, device=dev)
+            self.k_cache = torch.zeros(max(D.n_fa, 1), D.kv_heads, self.max_ctx, D.head_dim,
+                                       dtype=torch.float16 if kv_type == "f16" else torch.bfloat16, device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
         self.ssm_state = torch.zeros(max(D.n_dn, 1), D.dn_v_heads, D.dn_dim, D.dn_dim, dtype=torch.float32, device=dev)
         self.conv_state = torch.zeros(max(D.n_dn, 1), 3, D.conv_ch, dtype=torch.float32, device=dev)
@@ -195,7 +201,7 @@ class TreeTarget:
         a.node_argmax = self.node_argmax.data_ptr()
         a.scratch = self._scratch.data_ptr(); a.scratch_bytes = self._scratch.numel()
         a.dense_mask = self._dense_mask
-        a.kv_type = 1 if self.kv_type == "q8_0" else 0
+        a.kv_type = KV_TYPES[self.kv_type]
         if self.target_feat is not None:
             a.target_feat = self.target_feat.data_ptr(); a.feat_cap = self.feat_cap; a.n_capture = len(self.capture_layers)
             for i, il in enumerate(self.capture_layers):

@@ -83,14 +83,15 @@ def tree_verify_bench(dev, n_nodes=33, ctx=4096, iters=5, kv_type="bf16", n_laye
     w = make_random_tree_weights(T, 11, device=dev)
     tt = TreeTarget(T, w, max_ctx=ctx + 128, device=dev, kv_type=kv_type)
     g = torch.Generator(device=dev).manual_seed(11)
-    if kv_type == "q8_0":            # random Q8_0 rows: f16 d = 1/127 (bytes 0x08, 0x20), int8 values uniform
+    if kv_type in ("q8_0", "q4_0"):  # random quantised rows: f16 d = 1/127 (bytes 0x08, 0x20) or 1/8 (0x00, 0x30), codes uniform
         for c in (tt.k_cache, tt.v_cache):
-            blocks = c.view(-1, 34)
+            blocks = c.view(-1, 34 if kv_type == "q8_0" else 18)
             blocks.copy_(torch.randint(0, 256, blocks.shape, device=dev, generator=g, dtype=torch.uint8))
-            blocks[:, 0] = 0x08; blocks[:, 1] = 0x20
+            blocks[:, 0] = 0x08 if kv_type == "q8_0" else 0x00
+            blocks[:, 1] = 0x20 if kv_type == "q8_0" else 0x30
     else:
-        tt.k_cache.copy_(torch.randn(tt.k_cache.shape, device=dev, generator=g).bfloat16())
-        tt.v_cache.copy_(torch.randn(tt.v_cache.shape, device=dev, generator=g).bfloat16())
+        tt.k_cache.copy_(torch.randn(tt.k_cache.shape, device=dev, generator=g).to(tt.k_cache.dtype))
+        tt.v_cache.copy_(torch.randn(tt.v_cache.shape, device=dev, generator=g).to(tt.v_cache.dtype))
     tt.ssm_state.copy_(0.01 * torch.randn(tt.ssm_state.shape, device=dev, generator=g))
     tt.conv_state.copy_(0.1 * torch.randn(tt.conv_state.shape, device=dev, generator=g))
     parents = torch.tensor(random_tree(n_nodes, 8, 11), dtype=torch.int32, device=dev)
@@ -113,7 +114,7 @@ def tree_verify_bench(dev, n_nodes=33, ctx=4096, iters=5, kv_type="bf16", n_laye
     launches = (lib.qwen35_b200_launch_count() - l0) // (3 + iters)
     ms = min(times)
     w_bytes = (24_352_522_240 + 1_271_398_400) * 0.5625
-    kv_bytes = T.n_fa * T.kv_heads * (ctx + n_nodes) * (T.head_dim * 2 if kv_type == "bf16" else T.head_dim // 32 * 34) * 2
+    kv_bytes = T.n_fa * T.kv_heads * (ctx + n_nodes) * {"bf16": T.head_dim * 2, "f16": T.head_dim * 2, "q8_0": T.head_dim // 32 * 34, "q4_0": T.head_dim // 32 * 18}[kv_type] * 2
     st_bytes = T.n_dn * n_nodes * T.dn_v_heads * T.dn_dim * T.dn_dim * 2
     alg = w_bytes + kv_bytes + st_bytes
     flops = 2 * (24_352_522_240 + 1_271_398_400) * n_nodes

@@ -118,16 +118,55 @@ def q8_0_cache_value(x: torch.Tensor) -> torch.Tensor:
     return torch.from_numpy(q8_0_dequant(q8_0_quant(x.numpy())))
 
 
+def q4_0_quant(x: np.ndarray) -> np.ndarray:
+    """Q4_0 packing of f32 rows [..., 32k] -> uint8 [..., 18k]: per 32 elements, with m the element of largest magnitude
+    (the first one among equals, sign kept): f16 d = m / -8, q = min(15, trunc(x * (1 / d) + 8.5)) with the UNROUNDED f32 d
+    (d = 0 -> all q = 8), byte j = q[j] | q[j + 16] << 4, as ggml's quantize_row_q4_0_ref and gguf-py's
+    Q4_0.quantize_blocks do.  Pinned bit for bit to gguf-py 0.19.0 (tests/golden/q4_0_golden.npz)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    blk = x.reshape(-1, 32)
+    imax = np.abs(blk).argmax(axis=1)[:, None]
+    d = np.take_along_axis(blk, imax, axis=1) / np.float32(-8)
+    with np.errstate(divide="ignore"):
+        inv = np.where(d == 0, np.float32(0), np.float32(1) / d).astype(np.float32)
+    q = np.clip(np.trunc(blk * inv + np.float32(8.5)), 0, 15).astype(np.uint8)
+    out = np.empty((blk.shape[0], 18), np.uint8)
+    out[:, :2] = d.astype(np.float16).view(np.uint8).reshape(-1, 2)
+    out[:, 2:] = q[:, :16] | (q[:, 16:] << np.uint8(4))
+    return out.reshape(*x.shape[:-1], x.shape[-1] // 32 * 18)
+
+
+def q4_0_dequant(b: np.ndarray) -> np.ndarray:
+    """uint8 [..., 18k] -> f32 [..., 32k]: d (f16 -> f32) * (q - 8); low nibbles are elements 0..15, high nibbles 16..31."""
+    blk = np.ascontiguousarray(b, dtype=np.uint8).reshape(-1, 18)
+    d = blk[:, :2].copy().view(np.float16).astype(np.float32)
+    qs = blk[:, 2:]
+    q = np.concatenate([qs & np.uint8(15), qs >> np.uint8(4)], axis=1).astype(np.float32) - np.float32(8)
+    return (d * q).reshape(*b.shape[:-1], b.shape[-1] // 18 * 32)
+
+
+def kv_cache_value(x: torch.Tensor, kv_type: str) -> torch.Tensor:
+    """What a cache row of the given type written from f32 values x holds, as f32 (the attention reads it rounded to bf16)."""
+    if kv_type == "q8_0":
+        return q8_0_cache_value(x)
+    if kv_type == "q4_0":
+        return torch.from_numpy(q4_0_dequant(q4_0_quant(x.numpy())))
+    if kv_type == "f16":
+        return x.half().float()
+    raise ValueError(kv_type)
+
+
 def rb(x: torch.Tensor) -> torch.Tensor:
     return x.bfloat16().float()
 
 
 class TreeOracle:
-    def __init__(self, dims, weights, max_ctx, kv_q8=False):
-        """weights: the dict of qwen35_b200.tree_verify.make_random_tree_weights on the CPU.  kv_q8: the K / V cache is
-        Q8_0 (the reference's default, qwen35_target_graph.cpp:110-122): rows are quantised from their f32 values when
-        written and read back as bf16(d * q)."""
-        self.D, self.max_ctx, self.kv_q8 = dims, max_ctx, bool(kv_q8)
+    def __init__(self, dims, weights, max_ctx, kv_q8=False, kv_type=None):
+        """weights: the dict of qwen35_b200.tree_verify.make_random_tree_weights on the CPU.  kv_type: "bf16", or one of
+        the reference's cache types (qwen35_target_graph.cpp:110-122) "q8_0" (its default; kv_q8=True means the same),
+        "q4_0", "f16": rows are converted from their f32 values when written and read back rounded to bf16."""
+        self.D, self.max_ctx = dims, max_ctx
+        self.kv_type = kv_type or ("q8_0" if kv_q8 else "bf16")
         D = dims
 
         def mat(blocks):
@@ -197,8 +236,8 @@ class TreeOracle:
                 hn = lambda t, w: t * torch.rsqrt((t * t).mean(-1, keepdim=True) + D.rms_eps) * w      # noqa: E731
                 q = rb(self._rope(hn(q, W["q_norm"]), pos))
                 kk = self._rope(hn(kk, W["k_norm"]), pos)
-                if self.kv_q8:
-                    kk, vv = q8_0_cache_value(kk), q8_0_cache_value(vv)
+                if self.kv_type != "bf16":
+                    kk, vv = kv_cache_value(kk, self.kv_type), kv_cache_value(vv, self.kv_type)
                 else:
                     kk = rb(kk)
                 K = torch.cat([ctx["k"][i_fa], kk[:, None]], 1); V = torch.cat([ctx["v"][i_fa], vv[:, None]], 1)

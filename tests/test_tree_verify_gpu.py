@@ -469,3 +469,88 @@ def test_tree_verify_with_q8_0_kv_cache(n_ctx, n_nodes, seed):
             step = ref.reshape(ref.shape[0], ref.shape[1], -1, 32).abs().amax(-1, keepdim=True) / 127
             d = (got - ref).reshape(ref.shape[0], ref.shape[1], -1, 32).abs()
             assert bool((d <= step * 1.01 + 2.0 ** -5).all())          # the bf16 test's free-running bound plus one quantisation step
+
+
+@pytest.mark.parametrize("kv_type,n_ctx,n_nodes,seed", [("q4_0", 70, 14, 31), ("q4_0", 130, 33, 32), ("q4_0", 0, 5, 33),
+                                                        ("f16", 70, 14, 34), ("f16", 130, 33, 35)])
+def test_tree_verify_with_q4_0_and_f16_kv_cache(kv_type, n_ctx, n_nodes, seed):
+    """The reference's two other cache types (qwen35_target_graph.cpp:110-122): Q4_0 rows (quantised in the kernel from the
+    f32 row: d = the element of largest magnitude / -8, 4-bit codes) and F16 rows, both read back rounded to bf16.  Same
+    flow as the Q8_0 test against the oracle run with the same cache arithmetic."""
+    from oracle.tree_verify_oracle import TreeOracle, q4_0_dequant, q4_0_quant
+    from qwen35_b200.tree_verify import TreeTarget, make_random_tree_weights, random_tree
+    D = small_dims()
+    w = make_random_tree_weights(D, seed)
+    orc = TreeOracle(D, w, 256, kv_type=kv_type)
+    rng = np.random.default_rng(seed)
+    if n_ctx:
+        orc.feed(rng.integers(0, D.vocab, n_ctx))
+    wg = {"layers": [{k: v.cuda() for k, v in L.items()} for L in w["layers"]],
+          "token_embd": w["token_embd"].cuda(), "output_norm": w["output_norm"].cuda(), "output_w": w["output_w"].cuda()}
+    tt = TreeTarget(D, wg, max_ctx=256, kv_type=kv_type)
+    if kv_type == "q4_0":
+        assert tt.k_cache.dtype == torch.uint8 and tt.k_cache.shape[-1] == 144
+        to_cache = lambda x: torch.from_numpy(q4_0_quant(x.numpy()))                                   # noqa: E731
+        from_cache = lambda c: torch.from_numpy(q4_0_dequant(c.cpu().numpy()))                        # noqa: E731
+        step_of = lambda ref: ref.reshape(*ref.shape[:-1], -1, 32).abs().amax(-1, keepdim=True) / 8  # noqa: E731
+    else:
+        assert tt.k_cache.dtype == torch.float16 and tt.k_cache.shape[-1] == 256
+        to_cache = lambda x: x.half()                                                                  # noqa: E731
+        from_cache = lambda c: c.cpu().float()                                                         # noqa: E731
+        # an F16 row shows what the coarser types hide: one projection output (bf16) that the GEMM's summation order moved by a
+        # last place arrives, through the head norm and the rotation, as a difference of up to a bf16 last place of the
+        # largest element; such rows are counted below and must stay rare
+        step_of = lambda ref: ref.reshape(*ref.shape[:-1], -1, 32).abs().amax(-1, keepdim=True) * 2.0 ** -7   # noqa: E731
+    for i in range(D.n_fa):
+        if n_ctx:
+            # the oracle's committed rows are cache values already: packing them again gives back the same rows
+            tt.k_cache[i, :, :n_ctx] = to_cache(orc.k[i]).cuda()
+            tt.v_cache[i, :, :n_ctx] = to_cache(orc.v[i]).cuda()
+            assert torch.equal(from_cache(tt.k_cache[i, :, :n_ctx]), orc.k[i])
+    for i in range(D.n_dn):
+        tt.ssm_state[i] = orc.ssm[i].cuda(); tt.conv_state[i] = orc.conv[i].cuda()
+    tt.past = n_ctx
+    parents = random_tree(n_nodes, 6, seed)
+    tokens = rng.integers(0, D.vocab, n_nodes)
+    ref_logits, ctxs, hids = orc.verify(tokens, parents)
+    teacher = torch.zeros(D.n_layers, n_nodes, D.hidden, dtype=torch.bfloat16)
+    for t in range(n_nodes):
+        for il in range(1, D.n_layers):
+            teacher[il, t] = hids[t][il - 1].bfloat16()
+    dbg = torch.zeros(D.n_layers, n_nodes, D.hidden, dtype=torch.bfloat16, device="cuda")
+    tk, pr = torch.tensor(tokens, dtype=torch.int32), torch.tensor(parents, dtype=torch.int32)
+    tt.verify(tk, pr, dbg_hidden=dbg, dbg_teacher=teacher.cuda())
+    tt.check_status()
+    got_h = dbg.float().cpu()
+    ref_h = torch.stack([torch.stack(h) for h in hids]).transpose(0, 1)
+    assert float((got_h - ref_h).abs().max()) <= LAYER_ABS_TOL
+    print(f"{kv_type} cache, teacher forced: {float((got_h == ref_h).float().mean()):.4%} of layer outputs bit-identical")
+    # the rows the verify wrote (teacher forced, so their inputs equal the oracle's): node t sits at slot past + t.  An
+    # f32 last-place difference in a row's values may move one element across a rounding boundary (or, for Q4_0, change
+    # which of two near-equal magnitudes sets the block's scale: bounded by one step of the block)
+    flipped = total = 0
+    for i in range(D.n_fa):
+        for t in range(n_nodes):
+            for cache, key in ((tt.k_cache, "k"), (tt.v_cache, "v")):
+                ref = ctxs[t][key][i][:, -1]                                                         # [kv_heads, 256]
+                got = from_cache(cache[i, :, n_ctx + t])
+                d = (got - ref).reshape(ref.shape[0], -1, 32).abs()
+                assert bool((d <= step_of(ref) * 1.01 + 1e-6).all()), (i, t, key)
+                flipped += int((d > (1e-6 if kv_type == "q4_0" else ref.reshape(ref.shape[0], -1, 32).abs() * 2.0 ** -10 * 1.01 + 1e-7)).sum()); total += d.numel()
+    print(f"{kv_type} cache rows: {flipped}/{total} elements a step (F16: more than one f16 last place) from the oracle's")
+    assert flipped <= 0.02 * total
+    logits = torch.zeros(n_nodes, D.vocab, dtype=torch.bfloat16, device="cuda")
+    am = tt.verify(tk, pr, logits_out=logits).cpu().clone()
+    tt.check_status()
+    for t in range(n_nodes):
+        assert float((logits[t].float().cpu() - ref_logits[t]).abs().max()) <= LOGIT_TOL
+    path, result = tt.accept()
+    ref_path, ref_next = TreeOracle.accept(tokens, parents, am.tolist())
+    n_acc = tt.commit()
+    orc.commit(ctxs, ref_path)
+    assert n_acc == len(ref_path) and tt.past == orc.past
+    for i in range(D.n_fa):
+        for cache, ref in ((tt.k_cache, orc.k[i]), (tt.v_cache, orc.v[i])):
+            got = from_cache(cache[i, :, :tt.past])
+            d = (got - ref).reshape(ref.shape[0], ref.shape[1], -1, 32).abs()
+            assert bool((d <= step_of(ref) * 1.01 + 2.0 ** -5).all())          # the bf16 test's free-running bound plus one step
