@@ -38,7 +38,12 @@ constexpr int GEMM_BN_NARROW = 64, GEMM_STAGES_NARROW = 8, GEMM_STAGES_NARROW_SP
 // The epilogue parks the f32 accumulator tile in the (then idle) stage buffers as [row][GEMM_PARK_LD]: with a pitch of
 // 132 floats the float4 accesses of eight adjacent rows (writing, one row per thread) and of one row's adjacent column
 // groups (reading) both spread over all 32 banks.
-__host__ __device__ constexpr uint32_t gemm_park_bytes(int bn) { return (uint32_t)GEMM_BM * (bn + 4) * 4; }
+// The 256-column tile of the many-wave problems applies its epilogue arithmetic on the way out of tensor memory and parks
+// bf16 [row][GEMM_PARK_LD_WIDE] (a pitch of 132 words: the 16-byte stores of eight adjacent rows cover all 32 banks).
+constexpr int GEMM_BN_WIDE = 256, GEMM_STAGES_WIDE_TILE = 2, GEMM_PARK_LD_WIDE = GEMM_BN_WIDE + 8;
+__host__ __device__ constexpr uint32_t gemm_park_bytes(int bn) {
+    return bn == GEMM_BN_WIDE ? (uint32_t)GEMM_BM * GEMM_PARK_LD_WIDE * 2 : (uint32_t)GEMM_BM * (bn + 4) * 4;
+}
 __host__ __device__ constexpr uint32_t gemm_tile_bytes(int stages, int bn = GEMM_BN) {
     return stages * gemm_stage_bytes(bn) > gemm_park_bytes(bn) ? stages * gemm_stage_bytes(bn) : ((gemm_park_bytes(bn) + 1023u) & ~1023u);
 }
@@ -287,6 +292,45 @@ __device__ __forceinline__ void parked_tile_store(const GemmParams& p, uint32_t 
     }
 }
 
+// Store pass of a 256-column tile over its parked bf16 results [row][GEMM_PARK_LD_WIDE]: a work item is one row x 8 adjacent
+// output columns (16 bytes); consecutive threads take consecutive column groups of a row.  The residual is added here
+// (rounded sum + residual, rounded again: the same arithmetic as the narrower tiles).
+template <int EPI>
+__device__ __forceinline__ void parked_tile_store_wide(const GemmParams& p, const bf16* park, int rows, int m0, int n0, int t, int nt) {
+    constexpr int BN_OUT = (EPI == EPI_SILU_MUL) ? GEMM_BN_WIDE / 2 : GEMM_BN_WIDE;
+    constexpr int NG = BN_OUT / 8;
+    const int col = (t % NG) * 8, r_first = t / NG, r_step = nt / NG;
+    const bool vec_ok = n0 + col + 8 <= p.N && ((reinterpret_cast<uintptr_t>(p.C + n0 + col) | (size_t)p.ldc * 2) & 15) == 0 &&
+                        (EPI != EPI_RESIDUAL || ((reinterpret_cast<uintptr_t>(p.R + n0 + col) | (size_t)p.ldr * 2) & 15) == 0);
+    for (int r = r_first; r < rows; r += r_step) {
+        const uint4 v = *reinterpret_cast<const uint4*>(park + (size_t)r * GEMM_PARK_LD_WIDE + col);
+        if (vec_ok) {
+            uint4 o = v;
+            if (EPI == EPI_RESIDUAL) {
+                const uint4 res = *reinterpret_cast<const uint4*>(p.R + (size_t)(m0 + r) * p.ldr + n0 + col);
+                const uint32_t a[4] = {v.x, v.y, v.z, v.w}, b[4] = {res.x, res.y, res.z, res.w};
+                uint32_t c[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const __nv_bfloat162 pr = __halves2bfloat162(f2bf(bf_lo(a[j]) + bf_lo(b[j])), f2bf(bf_hi(a[j]) + bf_hi(b[j])));
+                    c[j] = *reinterpret_cast<const uint32_t*>(&pr);
+                }
+                o = make_uint4(c[0], c[1], c[2], c[3]);
+            }
+            *reinterpret_cast<uint4*>(p.C + (size_t)(m0 + r) * p.ldc + n0 + col) = o;
+        } else {
+            const uint32_t a[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (n0 + col + j < p.N) {
+                    float y = (j & 1) ? bf_hi(a[j >> 1]) : bf_lo(a[j >> 1]);
+                    if (EPI == EPI_RESIDUAL) y += bf2f(p.R[(size_t)(m0 + r) * p.ldr + n0 + col + j]);
+                    p.C[(size_t)(m0 + r) * p.ldc + n0 + col + j] = f2bf(y);
+                }
+        }
+    }
+}
+
 // SPLIT: gridDim.z = cluster size S along K (1, 2, 4 or 8); the cluster shares one output tile.  BN: columns of the tile.
 template <int EPI, int STAGES, bool SPLIT, int BN = GEMM_BN>
 __global__ void __launch_bounds__(GEMM_THREADS, gemm_ctas_per_sm(gemm_smem(STAGES, BN)))
@@ -306,7 +350,7 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
     constexpr uint32_t SB = gemm_stage_bytes(BN);
     // the B tile arrives as one or two boxes of B_BOX weight rows: the second box holds the rows that follow, or (SiLU
     // epilogue) the up-projection rows that belong to the tile's gate rows
-    constexpr int B_BOX = (BN == GEMM_BN) ? 64 : (EPI == EPI_SILU_MUL ? BN / 2 : BN), B_NBOX = BN / B_BOX;
+    constexpr int B_BOX = (BN == GEMM_BN) ? 64 : (BN == GEMM_BN_WIDE) ? 128 : (EPI == EPI_SILU_MUL ? BN / 2 : BN), B_NBOX = BN / B_BOX;
     const int n0 = blockIdx.x * BN_OUT, m0 = blockIdx.y * GEMM_BM;
     const int nkb_all = p.K / GEMM_BK;
     const int S = SPLIT ? (int)gridDim.z : 1, z = SPLIT ? (int)blockIdx.z : 0;
@@ -377,6 +421,39 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
         // warp-uniform, because tcgen05.ld is a warp-wide instruction
         const bool ok = __all_sync(0xffffffffu, g_mbar_wait(tfull, 0, p.err, s_abort) && !*s_abort);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (BN == GEMM_BN_WIDE) {
+            // 256-column tile: epilogue arithmetic here (a thread holds its row), results parked as bf16 for the store pass
+            bf16* parkh = reinterpret_cast<bf16*>(tiles_ptr) + (size_t)rloc * GEMM_PARK_LD_WIDE;
+            if (m0 + q * 32 < p.M) {
+#pragma unroll 1
+                for (int c = 0; c < BN_OUT / 32; ++c) {
+                    uint32_t v[32], w[32];
+                    if (ok) {
+                        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
+                        if (EPI == EPI_SILU_MUL) tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(BN / 2 + c * 32), w);
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; j += 8) {
+                        uint32_t o[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            float y0 = 0.f, y1 = 0.f;
+                            if (ok) {
+                                const float g0 = __uint_as_float(v[j + 2 * e]), g1 = __uint_as_float(v[j + 2 * e + 1]);
+                                if (EPI == EPI_SILU_MUL) {
+                                    y0 = rbf(silu_f(rbf(g0))) * rbf(__uint_as_float(w[j + 2 * e]));
+                                    y1 = rbf(silu_f(rbf(g1))) * rbf(__uint_as_float(w[j + 2 * e + 1]));
+                                } else { y0 = g0; y1 = g1; }
+                            }
+                            const __nv_bfloat162 pr = __halves2bfloat162(f2bf(y0), f2bf(y1));
+                            o[e] = *reinterpret_cast<const uint32_t*>(&pr);
+                        }
+                        *reinterpret_cast<uint4*>(parkh + c * 32 + j) = make_uint4(o[0], o[1], o[2], o[3]);
+                    }
+                }
+            }
+        } else {
         // park the f32 tile in the (now idle) stage buffers.  Split K: column-major [column][row], which makes the peers'
         // reads through distributed shared memory whole 128-byte lines (measured faster there than 16-byte pieces of rows);
         // one CTA per tile: row-major with a padded pitch, read back below as row segments.
@@ -401,6 +478,7 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
                 }
             }
         }
+        }
     }
     __syncwarp();
     if (SPLIT) {
@@ -414,7 +492,10 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
         // the store pass is arithmetic and address work on shared memory: all six warps take part (the copy and MMA warps
         // are idle by now)
         __syncthreads();
-        if (!*s_abort) parked_tile_store<EPI, BN>(p, tiles, min(GEMM_BM, p.M - m0), m0, n0, (int)threadIdx.x, GEMM_THREADS);
+        if (!*s_abort) {
+            if (BN == GEMM_BN_WIDE) parked_tile_store_wide<EPI>(p, reinterpret_cast<const bf16*>(tiles_ptr), min(GEMM_BM, p.M - m0), m0, n0, (int)threadIdx.x, GEMM_THREADS);
+            else parked_tile_store<EPI, BN>(p, tiles, min(GEMM_BM, p.M - m0), m0, n0, (int)threadIdx.x, GEMM_THREADS);
+        }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
@@ -826,13 +907,25 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
     while (split_n < GEMM_MAX_SPLIT && nt_n * split_n < 100 && nkb / (split_n * 2) >= 2) split_n *= 2;
     while (split_w < GEMM_MAX_SPLIT && n_tiles * split_w < 120 && nkb / (split_w * 2) >= 2) split_w *= 2;
     const bool narrow = m_tiles == 1 && n_tiles < 148 && (split_n == 1 || nkb <= 16 || nkb / split_n <= nkb / split_w);
-    const int b_box = !narrow ? 64 : (epi == EPI_SILU_MUL ? GEMM_BN_NARROW / 2 : GEMM_BN_NARROW);
+    // Many waves of tiles (long prompts x wide matrices): the 128 x 128 tile reads 32 KB from L2 per 128 x 128 x 64 step, and the
+    // SM's L2 port, shared by its two CTAs, is what bounds it.  A 128 x 256 tile reads 48 KB for twice the work (two CTAs of two
+    // stages per SM, 256 tensor-memory columns each).
+    const int bn_out_wd = (epi == EPI_SILU_MUL) ? GEMM_BN_WIDE / 2 : GEMM_BN_WIDE;
+    const int nt_wd = (N + bn_out_wd - 1) / bn_out_wd;
+    // Taken from 8 rows of tiles on, when its waves (two CTAs per SM) cost less than the 128-column tile's: a wave of the wide
+    // tile takes 1.8 x as long for twice the work (measured at 4096 x 8224 x 1024), and either form pays for a whole last wave.
+    const int slots_n = tiles_total <= 148 ? 148 : (tiles_total > 296 && tiles_total <= 444) ? 444 : 296;
+    const int waves_n = (tiles_total + slots_n - 1) / slots_n, waves_wd = (m_tiles * nt_wd + 295) / 296;
+    const bool wide_tile = !narrow && epi != EPI_RESIDUAL && m_tiles >= 8 && 18 * waves_wd < 10 * waves_n;
+    const int b_box = wide_tile ? 128 : !narrow ? 64 : (epi == EPI_SILU_MUL ? GEMM_BN_NARROW / 2 : GEMM_BN_NARROW);
     if (!make_tmap(&tmA, A, M, K, lda, GEMM_BM) || !make_tmap(&tmB, B, b_rows, K, K, b_box)) {
         set_error("cuTensorMapEncodeTiled failed (A %p [%d x %d] ld %d; B %p [%d x %d])", (const void*)A, M, K, lda, (const void*)B, b_rows, K);
         return QWEN35_ERR_CUDA;
     }
     int st = QWEN35_OK;
-    if (narrow) {
+    if (wide_tile) {
+        st = gemm_plain_epi<GEMM_STAGES_WIDE_TILE, GEMM_BN_WIDE>(epi, dim3(nt_wd, m_tiles), stream, tmA, tmB, p);
+    } else if (narrow) {
         if (split_n == 1) st = gemm_plain_epi<GEMM_STAGES_NARROW, GEMM_BN_NARROW>(epi, dim3(nt_n, 1), stream, tmA, tmB, p);
         else st = gemm_split_epi<GEMM_STAGES_NARROW_SPLIT, GEMM_BN_NARROW>(epi, dim3(nt_n, 1), split_n, stream, tmA, tmB, p);
     } else {

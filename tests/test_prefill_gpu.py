@@ -46,9 +46,11 @@ def _gemm(A, B, N, epi=0, R=None, up_off=0):
     return out
 
 
-# single-row-of-tiles shapes (M <= 128) run the narrow 16/32/64-column tiles; the others the 128-column tile
+# single-row-of-tiles shapes (M <= 128) run the narrow 64-column tiles, the last three (8 or more rows of tiles, fewer waves that way) the
+# 128 x 256 tile, the others the 128-column tile
 @pytest.mark.parametrize("M,N,K", [(1, 64, 64), (7, 96, 128), (128, 128, 1024), (520, 8224, 1024), (333, 1024, 3584), (1024, 5120, 1024),
-                                   (64, 1024, 2048), (64, 5120, 1024), (64, 8224, 1024), (33, 1000, 3584), (128, 20000, 1024)])
+                                   (64, 1024, 2048), (64, 5120, 1024), (64, 8224, 1024), (33, 1000, 3584), (128, 20000, 1024),
+                                   (1990, 8224, 1024), (4096, 5120, 2048), (3000, 4100, 64)])
 def test_gemm_plain(M, N, K):
     torch.manual_seed(M * 7 + N)
     A = torch.randn(M, K, device="cuda").bfloat16()
@@ -69,7 +71,7 @@ def test_gemm_fused_epilogues():
     got = _gemm(A, B, N, epi=1, R=R)
     ref = (A.float() @ B.float().t()).bfloat16() + R
     assert float((got != ref).float().mean()) <= GEMM_FLIP_FRAC
-    for M, N, K in ((130, 3584, 1024), (64, 3584, 1024), (64, 520, 1024), (16, 40, 128)):
+    for M, N, K in ((130, 3584, 1024), (64, 3584, 1024), (64, 520, 1024), (16, 40, 128), (2048, 3584, 1024), (1900, 3600, 128)):
         A = torch.randn(M, K, device="cuda").bfloat16()
         B = (torch.randn(2 * N, K, device="cuda") * 0.05).bfloat16()
         got = _gemm(A, B, N, epi=2, up_off=N)
