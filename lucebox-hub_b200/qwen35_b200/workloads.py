@@ -247,7 +247,7 @@ def decode_case(dev, prompt=64, gen=8, backend="bf16"):
     return {"prompt": prompt, "gen": gen, "backend": backend, "ms_per_token": e0.elapsed_time(e1) / gen, "tokens": toks.tolist()[:8]}
 
 
-def decode_stage_table(dev, ctx=520, gen=16):
+def decode_stage_table(dev, ctx=520, gen=16, backend="bf16"):
     """Per-stage time table of the bs=1 decode megakernel: the kernel records a clock64 stamp per CTA, layer and hand-off
     (dbg_time of the decode entry point); reported are medians over the 148 CTAs and over the layers of a kind, in
     microseconds at the 1965 MHz the kernel runs at, for the last of `gen` tokens decoded from a `ctx`-token position.
@@ -256,7 +256,7 @@ def decode_stage_table(dev, ctx=520, gen=16):
     from qwen35_b200.config import QWEN35_0P8B as D
     from qwen35_b200.model import Decoder
     from qwen35_b200.weights import make_random_weights, weights_to
-    dec = Decoder(weights=weights_to(make_random_weights(1234, D), dev), max_seq_len=2048, device=dev)
+    dec = Decoder(weights=weights_to(make_random_weights(1234, D), dev), max_seq_len=2048, device=dev, backend=backend)
     dec.reset(); dec._position = ctx
     for _ in range(2):
         dec.step_many(5, gen)
@@ -271,7 +271,7 @@ def decode_stage_table(dev, ctx=520, gen=16):
     dec.check_status()
     t = tl.cpu().numpy().astype(np.float64) / 1965.0
     names = ["start", "A.in", "A.pub", "B.pub", "C.in", "C.pub", "D.in", "D.pub", "E.in", "E.pub"]
-    out = {"us_per_token_untimed_run": us_per_token, "context": ctx}
+    out = {"us_per_token_untimed_run": us_per_token, "context": ctx, "weights": backend}
     for typ, tn in ((0, "deltanet"), (1, "attention")):
         rows = [l for l in range(4, 24) if D.layer_types[l] == typ]
         seg = {}
@@ -307,7 +307,7 @@ def main(argv=None):
     elif args.case == "draft_forward":
         out = draft_forward_bench(dev, ctx=args.ctx, iters=args.iters)
     elif args.case == "decode_stages":
-        out = decode_stage_table(dev, ctx=args.ctx if args.ctx != 256 else 520)
+        out = decode_stage_table(dev, ctx=args.ctx if args.ctx != 256 else 520, backend="nvfp4" if args.nvfp4 else "bf16")
     elif args.case == "decode":
         out = decode_case(dev, args.prompt, args.gen, "nvfp4" if args.nvfp4 else "bf16")
     else:
