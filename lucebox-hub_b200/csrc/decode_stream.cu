@@ -893,14 +893,16 @@ __global__ void __launch_bounds__(STREAM_THREADS, 1) decode_stream_kernel(const 
                     const bf16* hin = s.h;
                     const int u0 = s.pt[PT_C0], nt = s.pt[PT_C1] - u0;
                     if (FP4) {
-                        // 4 rows x 1024 bytes of nibbles per tile; warps 0-7: row w/2, K half w%2 (32 groups of 32, one per lane)
+                        // 4 rows x 1024 bytes of nibbles per tile, two tiles at a time: warp = (tile w/8, row (w/2)%4, K half w%2), 32
+                        // groups of 32 per half row, one per lane
                         float x[32];
-                        if (warp < 8) load_x32(s.x, (warp & 1) * 1024 + 32 * lane, x);
-                        for (int ti = 0; ti < nt; ++ti) {
-                            const unsigned tile = ring.t + (unsigned)ti;
-                            if (warp < 8) {
+                        load_x32(s.x, (warp & 1) * 1024 + 32 * lane, x);
+                        const uint32_t row = (uint32_t)((warp >> 1) & 3), half = (uint32_t)(warp & 1);
+                        for (int tb = 0; tb < nt; tb += 2) {
+                            const int ti = tb + (warp >> 3);
+                            if (ti < nt) {
+                                const unsigned tile = ring.t + (unsigned)ti;
                                 mbar_wait(ring.full_bar(tile), ring.phase(tile), ab);
-                                const uint32_t row = (uint32_t)(warp >> 1), half = (uint32_t)(warp & 1);
                                 const uint4 pk = lds128(ring.slot_addr(tile) + row * 1024u + half * 512u + (uint32_t)lane * 16u);
                                 const float sc = lds_half(ring.slot_addr(tile) + FP4_SCALE_OFF + row * 128u + (half * 32u + (uint32_t)lane) * 2u);
                                 const float acc = warp_sum(dot32_fp4(pk, x) * sc);
