@@ -16,7 +16,8 @@
 //   warp 1   allocates tensor memory; one thread copies the 8 scale atoms of the stage into tensor memory and issues the
 //            four K = 64 instructions, then commits the stage back to the producer
 //   warps 2-5 epilogue: tcgen05.ld rows of the accumulator (lane = weight row, column = token), scale, round once to bf16
-//            (or keep f32), optional residual, transposed store C[token][weight row]
+//            and park the tile transposed, [token][weight row], in the idle stage buffers; then all six warps store whole
+//            rows of C (16 bytes per thread, residual added there).  f32 output (the 16-row LM head) is stored directly.
 // Every wait is bounded; a wait that runs out sets the status word and the CTA unwinds normally.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -31,7 +32,11 @@ namespace q35 {
 
 constexpr int FP4_BM = 128;                     // weight rows per CTA
 constexpr int FP4_BK = 256;                     // elements of K per stage = 128 bytes of packed nibbles per row
-constexpr int FP4_STAGES = 4;
+// stages per CTA: three of 36 KB for the 128-token tile, so that two CTAs share an SM (the epilogue of one tile runs under the
+// main loop of another; 256 tensor-memory columns each), four for the narrower tiles
+__host__ __device__ constexpr int fp4_stages(int t_tile) { return t_tile >= 128 ? 3 : 4; }
+// bf16 results are parked [token][FP4_PARK_LD] in the idle stage buffers and stored as whole rows
+constexpr int FP4_PARK_LD = FP4_BM + 8;
 constexpr int FP4_THREADS = 192;
 constexpr uint32_t FP4_W_BYTES = FP4_BM * 128;  // 16 KB
 constexpr uint32_t FP4_SF_BYTES = 4 * 512;      // four K-atoms of scales per stage and operand
@@ -39,7 +44,12 @@ constexpr unsigned FP4_SPIN_LIMIT = 20u * 1000u * 1000u;
 constexpr uint32_t FP4_TMEM_COLS = 256;         // accumulator (<= 128) + two alternating sets of 32 scale columns
 
 __host__ __device__ constexpr uint32_t fp4_stage_bytes(int t_tile) { return FP4_W_BYTES + (uint32_t)t_tile * 128u + 2u * FP4_SF_BYTES; }
-__host__ __device__ constexpr uint32_t fp4_smem(int t_tile) { return FP4_STAGES * fp4_stage_bytes(t_tile) + 1024 + 256; }
+__host__ __device__ constexpr uint32_t fp4_park_bytes(int t_tile) { return (uint32_t)t_tile * FP4_PARK_LD * 2u; }
+__host__ __device__ constexpr uint32_t fp4_tile_bytes(int t_tile) {
+    return fp4_stages(t_tile) * fp4_stage_bytes(t_tile) > fp4_park_bytes(t_tile) ? fp4_stages(t_tile) * fp4_stage_bytes(t_tile)
+                                                                                  : ((fp4_park_bytes(t_tile) + 1023u) & ~1023u);
+}
+__host__ __device__ constexpr uint32_t fp4_smem(int t_tile) { return fp4_tile_bytes(t_tile) + 1024 + 256; }
 
 struct Fp4GemmParams {
     int T, N, K;                 // tokens, output columns (<= the weight rows the tensor map covers), reduction length
@@ -83,16 +93,17 @@ __device__ __forceinline__ uint32_t f_idesc(int n) {
 }
 
 template <int T_TILE>
-__global__ void __launch_bounds__(FP4_THREADS, 1)
+__global__ void __launch_bounds__(FP4_THREADS, 2)
 gemm_nvfp4_tcgen05_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmA, const Fp4GemmParams p) {
     static_assert(T_TILE % 16 == 0 && T_TILE >= 16 && T_TILE <= 128, "token tile: a multiple of 16 up to 128");
     constexpr uint32_t STAGE = fp4_stage_bytes(T_TILE);
+    constexpr int FP4_STAGES = fp4_stages(T_TILE);
     constexpr uint32_t A_OFF = FP4_W_BYTES, SFW_OFF = A_OFF + T_TILE * 128u, SFA_OFF = SFW_OFF + FP4_SF_BYTES;
     extern __shared__ unsigned char f_smem_raw[];
     const uint32_t raw = f_smem_u32(f_smem_raw);
     const uint32_t tiles = (raw + 1023u) & ~1023u;                 // swizzled tiles need 1024-byte alignment
     unsigned char* tiles_ptr = f_smem_raw + (tiles - raw);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(tiles_ptr + FP4_STAGES * STAGE);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(tiles_ptr + fp4_tile_bytes(T_TILE));
     const uint32_t full0 = f_smem_u32(bars), empty0 = full0 + 8 * FP4_STAGES, tfull = empty0 + 8 * FP4_STAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * FP4_STAGES + 1);
     volatile int* s_abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -186,6 +197,7 @@ gemm_nvfp4_tcgen05_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_
         const bool ok = __all_sync(0xffffffffu, f_wait(tfull, 0, p.err, s_abort) && !*s_abort);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (ok) {
+            bf16* park = reinterpret_cast<bf16*>(tiles_ptr);
 #pragma unroll
             for (int c = 0; c < T_TILE / 16; ++c) {
                 uint32_t v[16];
@@ -195,22 +207,58 @@ gemm_nvfp4_tcgen05_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_
                       "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
                     : "r"(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 16)) : "memory");
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                if (col < p.N) {
+                if (p.out_f32) {
+                    if (col < p.N) {
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int tok = t0 + c * 16 + j;
-                        if (tok < p.T) {
-                            const float y = __uint_as_float(v[j]) * p.alpha;
-                            if (p.out_f32) {
-                                reinterpret_cast<float*>(p.C)[(size_t)tok * p.ldc + col] = y;
-                            } else {
-                                float r = rbf(y);
-                                if (p.R) r += bf2f(p.R[(size_t)tok * p.ldr + col]);
-                                reinterpret_cast<bf16*>(p.C)[(size_t)tok * p.ldc + col] = f2bf(r);
-                            }
+                        for (int j = 0; j < 16; ++j) {
+                            const int tok = t0 + c * 16 + j;
+                            if (tok < p.T) reinterpret_cast<float*>(p.C)[(size_t)tok * p.ldc + col] = __uint_as_float(v[j]) * p.alpha;
                         }
                     }
+                } else {
+                    // the 32 lanes of a warp write 32 adjacent bf16 of one token's row: conflict-free
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) park[(c * 16 + j) * FP4_PARK_LD + q * 32 + lane] = f2bf(__uint_as_float(v[j]) * p.alpha);
                 }
+            }
+        }
+    }
+    __syncthreads();                                              // the parked tile is complete (all warps pass here, whatever happened)
+    if (!p.out_f32 && !*s_abort) {
+        // ---- store pass, all six warps: a work item is one token x 8 adjacent output columns (16 bytes) ----
+        const bf16* park = reinterpret_cast<const bf16*>(tiles_ptr);
+        constexpr int NG = FP4_BM / 8;
+        const int t = (int)threadIdx.x, cg = (t % NG) * 8, r_first = t / NG, r_step = FP4_THREADS / NG;
+        const int rows = min(T_TILE, p.T - t0);
+        bf16* cbase = reinterpret_cast<bf16*>(p.C);
+        const bool vec_ok = n0 + cg + 8 <= p.N && ((reinterpret_cast<uintptr_t>(cbase + n0 + cg) | (size_t)p.ldc * 2) & 15) == 0 &&
+                            (!p.R || ((reinterpret_cast<uintptr_t>(p.R + n0 + cg) | (size_t)p.ldr * 2) & 15) == 0);
+        for (int r = r_first; r < rows; r += r_step) {
+            const uint4 v = *reinterpret_cast<const uint4*>(park + r * FP4_PARK_LD + cg);
+            const size_t tok = (size_t)(t0 + r);
+            if (vec_ok) {
+                uint4 o = v;
+                if (p.R) {
+                    const uint4 res = *reinterpret_cast<const uint4*>(p.R + tok * p.ldr + n0 + cg);
+                    const uint32_t a[4] = {v.x, v.y, v.z, v.w}, b[4] = {res.x, res.y, res.z, res.w};
+                    uint32_t cc[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const __nv_bfloat162 pr = __halves2bfloat162(f2bf(bf_lo(a[j]) + bf_lo(b[j])), f2bf(bf_hi(a[j]) + bf_hi(b[j])));
+                        cc[j] = *reinterpret_cast<const uint32_t*>(&pr);
+                    }
+                    o = make_uint4(cc[0], cc[1], cc[2], cc[3]);
+                }
+                *reinterpret_cast<uint4*>(cbase + tok * p.ldc + n0 + cg) = o;
+            } else {
+                const uint32_t a[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    if (n0 + cg + j < p.N) {
+                        float y = (j & 1) ? bf_hi(a[j >> 1]) : bf_lo(a[j >> 1]);
+                        if (p.R) y += bf2f(p.R[tok * p.ldr + n0 + cg + j]);
+                        cbase[tok * p.ldc + n0 + cg + j] = f2bf(y);
+                    }
             }
         }
     }
