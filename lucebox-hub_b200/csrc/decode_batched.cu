@@ -604,7 +604,7 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
         if (layer > 0 && in->dbg_teacher)
             Q35_CUDA_OK(pdl_launch(bd_copy_rows_kernel, (int)((n_hidden / 8 + 255) / 256), 256, 0, stream, (const bf16*)in->dbg_teacher + (size_t)layer * n_hidden, hidden, (int)(n_hidden / 8)));
         Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, B, 128, 0, stream, layer == 0 ? in->tokens_in : nullptr, (const bf16*)in->embed_weight, hidden, (const bf16*)L.p[0],
-                                                 layer == 0 ? hidden : nullptr, normed, B));
+                                                 layer == 0 ? hidden : nullptr, normed, B, (uint8_t*)nullptr, (uint8_t*)nullptr));
         const bf16 *w_out, *w_post, *w_down;
         if (L.type == 0) {
             const int ldp = DN_PROJ_ROWS;
@@ -645,14 +645,14 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
             ++i_fa;
         }
         Q35_TRYB(gemm_bf16(attn, 2048, w_out, HIDDEN, resid, HIDDEN, hidden, HIDDEN, B, HIDDEN, 2048, 1, 0, stream));
-        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, B, 128, 0, stream, nullptr, nullptr, resid, w_post, nullptr, normed, B));
+        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, B, 128, 0, stream, nullptr, nullptr, resid, w_post, nullptr, normed, B, (uint8_t*)nullptr, (uint8_t*)nullptr));
         Q35_TRYB(gemm_bf16(normed, HIDDEN, (const bf16*)F.gate_up_weight, 2 * INTER, mlp, INTER, nullptr, 0, B, INTER, HIDDEN, 2, INTER, stream));
         Q35_TRYB(gemm_bf16(mlp, INTER, w_down, HIDDEN, hidden, HIDDEN, resid, HIDDEN, B, HIDDEN, INTER, 1, 0, stream));
         g_launches.fetch_add(2);
         if (in->dbg_hidden)
             Q35_CUDA_OK(pdl_launch(bd_copy_rows_kernel, (int)((n_hidden / 8 + 255) / 256), 256, 0, stream, hidden, (bf16*)in->dbg_hidden + (size_t)layer * n_hidden, (int)(n_hidden / 8)));
     }
-    Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, B, 128, 0, stream, nullptr, nullptr, hidden, (const bf16*)in->final_norm_weight, nullptr, normed, B));
+    Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, B, 128, 0, stream, nullptr, nullptr, hidden, (const bf16*)in->final_norm_weight, nullptr, normed, B, (uint8_t*)nullptr, (uint8_t*)nullptr));
     Q35_TRYB(gemm_bf16(normed, HIDDEN, (const bf16*)in->lm_head_weight, VOCAB, logits, VOCAB, nullptr, 0, B, VOCAB, HIDDEN, 0, 0, stream));
     Q35_CUDA_OK(pdl_launch(bd_argmax_kernel, B, 1024, 0, stream, logits, in->tokens_out, in->advance_positions ? in->positions : nullptr, in->max_ctx));
     if (in->logits_out) Q35_CUDA_OK(cudaMemcpyAsync(in->logits_out, logits, n_logits * sizeof(bf16), cudaMemcpyDeviceToDevice, stream));

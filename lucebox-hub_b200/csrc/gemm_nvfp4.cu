@@ -26,6 +26,7 @@
 #include <cuda_fp8.h>
 
 #include "common.cuh"
+#include "nvfp4_act.cuh"
 #include "runtime.h"
 
 namespace q35 {
@@ -285,23 +286,11 @@ __global__ void __launch_bounds__(256) quantize_act_nvfp4_kernel(const bf16* __r
             const uint4 v0 = src[0], v1 = src[1];
             wd[0] = v0.x; wd[1] = v0.y; wd[2] = v0.z; wd[3] = v0.w; wd[4] = v1.x; wd[5] = v1.y; wd[6] = v1.z; wd[7] = v1.w;
         }
-        float amax = 0.f;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fmaxf(fabsf(bf_lo(wd[k])), fabsf(bf_hi(wd[k]))));
-        const float scale_f = fmaxf(__fmul_rn(amax, 1.0f / 6.0f), 1.0f / (float)(1 << 28));
-        const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(scale_f, __NV_SATFINITE, __NV_E4M3);
-        const __half_raw hr = __nv_cvt_fp8_to_halfraw(s8, __NV_E4M3);
-        const float dec = __half2float(*reinterpret_cast<const __half*>(&hr));
-        const float inv = (dec > 0.f) ? __fdiv_rn(1.0f, dec) : 0.f;
-        unsigned long long out = 0;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const float2 f2 = make_float2(__fmul_rn(bf_lo(wd[k]), inv), __fmul_rn(bf_hi(wd[k]), inv));
-            out |= (unsigned long long)(uint8_t)__nv_cvt_float2_to_fp4x2(f2, __NV_E2M1, cudaRoundNearest) << (8 * k);
-        }
-        *reinterpret_cast<unsigned long long*>(packed + row * (K / 2) + sc * 8) = out;
-        const long long tile = (row >> 7) * (K / 64) + (sc >> 2);
-        scales[tile * 512 + (row & 31) * 16 + ((row & 127) >> 5) * 4 + (sc & 3)] = (uint8_t)s8;
+        const uint32_t lo4[4] = {wd[0], wd[1], wd[2], wd[3]}, hi4[4] = {wd[4], wd[5], wd[6], wd[7]};
+        float inv;
+        const uint8_t s8 = nvfp4_act_scale(fmaxf(nvfp4_amax8(lo4), nvfp4_amax8(hi4)), inv);
+        *reinterpret_cast<uint2*>(packed + row * (K / 2) + sc * 8) = make_uint2(nvfp4_pack8(lo4, inv), nvfp4_pack8(hi4, inv));
+        scales[nvfp4_scale_index(row, sc, K)] = s8;
     }
 }
 

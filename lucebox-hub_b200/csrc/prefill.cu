@@ -83,6 +83,7 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
     // atoms) and one row of bf16 logits for the tensor-core FP4 head
     const size_t chunk_bytes = ((size_t)DN_HEADS * nchunks * sizeof(ChunkScratch) + 255) & ~(size_t)255;
     const size_t tpad = ((size_t)S + 127) / 128 * 128;
+    const int s_pad = (int)tpad;               // rows of the packed NVFP4 activation operand
     const size_t act_packed_bytes = tpad * (HIDDEN / 2), act_scale_bytes = tpad / 128 * (HIDDEN / 64) * 512;
     const size_t head_bytes = (chunk_bytes + act_packed_bytes + act_scale_bytes + (size_t)VOCAB * 2 + 256 + 1023) & ~(size_t)1023;
     char* scratch_base = (char*)get_scratch(head_bytes + attention_tcgen05_scratch_bytes(S) + 1024);
@@ -109,14 +110,15 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
         // input norm (layer 0 gathers the embedding rows into `hidden` on the way); with a teacher, layer l > 0 takes its
         // input (and the residual of its mixer) from the teacher's row block instead of the previous layer's output
         const bf16* layer_in = (a.dbg_teacher && layer > 0) ? a.dbg_teacher + (size_t)layer * S * HIDDEN : a.hidden;
-        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, S, 128, 0, stream, layer == 0 ? a.token_ids : nullptr, a.embed, layer_in, (const bf16*)L.p[0],
-                                                 layer == 0 ? a.hidden : nullptr, a.normalized, S));
+        // (NVFP4: the kernel packs the normalised rows as the activation operand on the way out, and the bf16 copy is not written)
+        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, fp4 ? s_pad : S, 128, 0, stream, layer == 0 ? a.token_ids : nullptr, a.embed, layer_in, (const bf16*)L.p[0],
+                                                 layer == 0 ? a.hidden : nullptr, fp4 ? (bf16*)nullptr : a.normalized, S,
+                                                 fp4 ? (uint8_t*)act_packed : (uint8_t*)nullptr, fp4 ? (uint8_t*)act_scales : (uint8_t*)nullptr));
         g_launches.fetch_add(1);
         const bf16 *w_out, *w_post, *w_down;
         if (L.type == 0) {
             const int ldp = DN_PROJ_ROWS;
             if (fp4) {
-                Q35_TRY(quantize_act_nvfp4(a.normalized, S, HIDDEN, act_packed, act_scales, stream));
                 Q35_TRY(gemm_nvfp4(act_packed, act_scales, S, F->proj_packed, F->proj_scales, (DN_PROJ_ROWS + 127) / 128 * 128, DN_PROJ_ROWS, HIDDEN, 1.0f,
                                    a.proj_buf, ldp, 0, nullptr, 0, stream));
             } else if (F) {
@@ -139,7 +141,6 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
         } else {
             const int ldp = FA_PROJ_ROWS;
             if (fp4) {
-                Q35_TRY(quantize_act_nvfp4(a.normalized, S, HIDDEN, act_packed, act_scales, stream));
                 Q35_TRY(gemm_nvfp4(act_packed, act_scales, S, F->proj_packed, F->proj_scales, FA_PROJ_ROWS, FA_PROJ_ROWS, HIDDEN, 1.0f, a.proj_buf, ldp, 0,
                                    nullptr, 0, stream));
             } else if (F) {
@@ -160,11 +161,11 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
         }
         // output projection + residual -> residual buffer holds the hidden state after the mixer
         Q35_TRY(gemm_bf16(a.attn_buf, 2048, w_out, HIDDEN, a.residual, HIDDEN, layer_in, HIDDEN, S, HIDDEN, 2048, 1, 0, stream));
-        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, S, 128, 0, stream, nullptr, nullptr, a.residual, w_post, nullptr, a.normalized, S));
+        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, fp4 ? s_pad : S, 128, 0, stream, nullptr, nullptr, a.residual, w_post, nullptr, fp4 ? (bf16*)nullptr : a.normalized, S,
+                                                 fp4 ? (uint8_t*)act_packed : (uint8_t*)nullptr, fp4 ? (uint8_t*)act_scales : (uint8_t*)nullptr));
         g_launches.fetch_add(1);
         if (fp4) {
             // [gate | up] rows of one block-scaled GEMM into proj_buf ([S, 7168]; the projection buffer is free again), then SiLU * up
-            Q35_TRY(quantize_act_nvfp4(a.normalized, S, HIDDEN, act_packed, act_scales, stream));
             Q35_TRY(gemm_nvfp4(act_packed, act_scales, S, F->gate_up_packed, F->gate_up_scales, 2 * INTER, 2 * INTER, HIDDEN, 1.0f, a.proj_buf, 2 * INTER, 0,
                                nullptr, 0, stream));
             Q35_CUDA_OK(pdl_launch(pf_silu_mul_rows_kernel, (S * (INTER / 8) + 255) / 256, 256, 0, stream, (const bf16*)a.proj_buf, a.mlp_buf, S));
@@ -187,12 +188,12 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
     // last token: final norm, LM head, arg-max
     const bf16* last = a.hidden + (size_t)(S - 1) * HIDDEN;
     if (a.hidden_out) Q35_CUDA_OK(cudaMemcpyAsync(a.hidden_out, last, HIDDEN * sizeof(bf16), cudaMemcpyDeviceToDevice, stream));
-    Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, 1, 128, 0, stream, nullptr, nullptr, last, a.final_norm, nullptr, a.final_normed, 1));
+    Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, a.lm_packed ? 128 : 1, 128, 0, stream, nullptr, nullptr, last, a.final_norm, nullptr, a.final_normed, 1,
+                                             a.lm_packed ? (uint8_t*)act_packed : (uint8_t*)nullptr, a.lm_packed ? (uint8_t*)act_scales : (uint8_t*)nullptr));
     const int lm_blocks = 592;
     if (a.lm_packed) {
         // the reference's FP4 head (kernel_gb10_nvfp4.cu:1945-1997): the normed hidden row is quantised to NVFP4 as well and the
         // block-scaled tensor-core GEMM gives the logits, rounded once to bf16; arg-max with the lowest index among ties
-        Q35_TRY(quantize_act_nvfp4(a.final_normed, 1, HIDDEN, act_packed, act_scales, stream));
         Q35_TRY(gemm_nvfp4(act_packed, act_scales, 1, a.lm_packed, a.lm_scales, VOCAB, VOCAB, HIDDEN, 1.0f, lm_logits, VOCAB, 0, nullptr, 0, stream));
         Q35_CUDA_OK(pdl_launch(pf_argmax_row_kernel, 1, 1024, 0, stream, (const bf16*)lm_logits, a.out_token, a.logits_out));
         g_launches.fetch_add(2);

@@ -15,19 +15,30 @@
 #include <cuda_fp8.h>
 
 #include "common.cuh"
+#include "nvfp4_act.cuh"
 
 namespace q35 {
 
 constexpr int DN_CHUNK = 64;
 
 // ---- one CTA (128 threads) per token: optional embedding gather, RMSNorm(1+w) -------------------
-// h_out (may be null) receives the raw row; x_out the normalised row.
+// h_out (may be null) receives the raw row; x_out (may be null) the normalised row.  With q_packed / q_scales the normalised
+// row is also packed as the NVFP4 activation operand of the GEMM that follows (a block of 16 elements is two threads; the
+// grid then covers the rows up to the next multiple of 128, and the rows from S on are written as zeros).
 static __global__ void __launch_bounds__(128) pf_rmsnorm_kernel(const int* __restrict__ ids, const bf16* __restrict__ embed,
                                                          const bf16* __restrict__ h_in, const bf16* __restrict__ w,
-                                                         bf16* __restrict__ h_out, bf16* __restrict__ x_out, int S) {
+                                                         bf16* __restrict__ h_out, bf16* __restrict__ x_out, int S,
+                                                         uint8_t* __restrict__ q_packed, uint8_t* __restrict__ q_scales) {
     pdl_wait();
     __shared__ float red[4];
     const int t = blockIdx.x, tid = threadIdx.x;
+    if (t >= S) {                   // padding rows of the packed operand
+        if (q_packed) {
+            reinterpret_cast<uint32_t*>(q_packed + (size_t)t * (HIDDEN / 2))[tid] = 0u;
+            if (!(tid & 1)) q_scales[nvfp4_scale_index(t, tid >> 1, HIDDEN)] = 0;
+        }
+        return;
+    }
     const bf16* src = ids ? embed + (size_t)ids[t] * HIDDEN : h_in + (size_t)t * HIDDEN;
     const uint4 raw = *(reinterpret_cast<const uint4*>(src) + tid);
     if (h_out) *(reinterpret_cast<uint4*>(h_out + (size_t)t * HIDDEN) + tid) = raw;
@@ -50,7 +61,14 @@ static __global__ void __launch_bounds__(128) pf_rmsnorm_kernel(const int* __res
         const __nv_bfloat162 p = __halves2bfloat162(f2bf((x[2 * i] * r) * (1.0f + wv[2 * i])), f2bf((x[2 * i + 1] * r) * (1.0f + wv[2 * i + 1])));
         o[i] = *reinterpret_cast<const uint32_t*>(&p);
     }
-    *(reinterpret_cast<uint4*>(x_out + (size_t)t * HIDDEN) + tid) = make_uint4(o[0], o[1], o[2], o[3]);
+    if (x_out) *(reinterpret_cast<uint4*>(x_out + (size_t)t * HIDDEN) + tid) = make_uint4(o[0], o[1], o[2], o[3]);
+    if (q_packed) {
+        const float a8 = nvfp4_amax8(o);
+        float inv;
+        const uint8_t s8 = nvfp4_act_scale(fmaxf(a8, __shfl_xor_sync(0xffffffffu, a8, 1)), inv);
+        reinterpret_cast<uint32_t*>(q_packed + (size_t)t * (HIDDEN / 2))[tid] = nvfp4_pack8(o, inv);
+        if (!(tid & 1)) q_scales[nvfp4_scale_index(t, tid >> 1, HIDDEN)] = s8;
+    }
 }
 
 // ---- silu(gate) * up over [S, INTER] bf16 buffers, 8 values per thread: the epilogue of the fused [gate; up] GEMM as a
