@@ -906,7 +906,19 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
     int split_n = 1, split_w = 1;
     while (split_n < GEMM_MAX_SPLIT && nt_n * split_n < 100 && nkb / (split_n * 2) >= 2) split_n *= 2;
     while (split_w < GEMM_MAX_SPLIT && n_tiles * split_w < 120 && nkb / (split_w * 2) >= 2) split_w *= 2;
-    const bool narrow = m_tiles == 1 && n_tiles < 148 && (split_n == 1 || nkb <= 16 || nkb / split_n <= nkb / split_w);
+    bool narrow = m_tiles == 1 && n_tiles < 148 && (split_n == 1 || nkb <= 16 || nkb / split_n <= nkb / split_w);
+    // A few rows of tiles with long K (the out / down projections of a 1024-token prompt: 64 tiles of 128 columns): where the
+    // 128-column tiles with their split leave SMs without a CTA, 64-column tiles with the same rule fill them (4.33 -> 4.19 ms
+    // for the 1024-token prompt), and so they do where the wide form would need 8-CTA clusters and they need 4 (260 tokens:
+    // 2.30 -> 2.23 ms); where the wide form already has a CTA per SM with clusters of 4 it stays (520 tokens: 160 CTAs either
+    // way, and the wide form is the faster one there).
+    int m_rows_n = 1;
+    if (!narrow && m_tiles > 1 && tiles_total < 100 && nkb >= 16) {
+        int sw = 1, sp = 1;
+        while (sw < GEMM_MAX_SPLIT && tiles_total * sw < 120 && nkb / (sw * 2) >= 2) sw *= 2;
+        while (sp < GEMM_MAX_SPLIT && nt_n * m_tiles * sp < 148 && nkb / (sp * 2) >= 2) sp *= 2;
+        if (sp >= 2 && ((tiles_total * sw < 148 && nt_n * m_tiles * sp > tiles_total * sw) || (sw >= 8 && sp < sw))) { narrow = true; split_n = sp; m_rows_n = m_tiles; }
+    }
     // Many waves of tiles (long prompts x wide matrices): the 128 x 128 tile reads 32 KB from L2 per 128 x 128 x 64 step, and the
     // SM's L2 port, shared by its two CTAs, is what bounds it.  A 128 x 256 tile reads 48 KB for twice the work (two CTAs of two
     // stages per SM, 256 tensor-memory columns each).
@@ -927,7 +939,7 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
         st = gemm_plain_epi<GEMM_STAGES_WIDE_TILE, GEMM_BN_WIDE>(epi, dim3(nt_wd, m_tiles), stream, tmA, tmB, p);
     } else if (narrow) {
         if (split_n == 1) st = gemm_plain_epi<GEMM_STAGES_NARROW, GEMM_BN_NARROW>(epi, dim3(nt_n, 1), stream, tmA, tmB, p);
-        else st = gemm_split_epi<GEMM_STAGES_NARROW_SPLIT, GEMM_BN_NARROW>(epi, dim3(nt_n, 1), split_n, stream, tmA, tmB, p);
+        else st = gemm_split_epi<GEMM_STAGES_NARROW_SPLIT, GEMM_BN_NARROW>(epi, dim3(nt_n, m_rows_n), split_n, stream, tmA, tmB, p);
     } else {
         // a grid that cannot fill the SMs (few tiles, long K) splits K over clusters
         const bool small_grid = tiles_total < 100 && nkb >= 8;

@@ -79,13 +79,14 @@ def test_gemm_fused_epilogues():
         u = (A.float() @ B[N:].float().t()).bfloat16()
         ref = torch.nn.functional.silu(g) * u
         assert float((got != ref).float().mean()) <= 2 * GEMM_FLIP_FRAC, (M, N, K)
-    M, N, K = 64, 1024, 3584
-    A = torch.randn(M, K, device="cuda").bfloat16()
-    B = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
-    R = torch.randn(M, N, device="cuda").bfloat16()
-    got = _gemm(A, B, N, epi=1, R=R)
-    ref = (A.float() @ B.float().t()).bfloat16() + R
-    assert float((got != ref).float().mean()) <= GEMM_FLIP_FRAC
+    # one row of tiles, and several rows of 64-column tiles with K split over clusters (3, 4 and 8 rows of tiles)
+    for M, N, K in ((64, 1024, 3584), (260, 1024, 2048), (512, 1024, 3584), (1000, 1024, 2048)):
+        A = torch.randn(M, K, device="cuda").bfloat16()
+        B = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+        R = torch.randn(M, N, device="cuda").bfloat16()
+        got = _gemm(A, B, N, epi=1, R=R)
+        ref = (A.float() @ B.float().t()).bfloat16() + R
+        assert float((got != ref).float().mean()) <= GEMM_FLIP_FRAC, (M, N, K)
 
 
 def test_gemm_rejects_bad_shapes():
