@@ -532,6 +532,9 @@ constexpr int Q4K_STAGES = 3, Q4K_RAW_STAGES = 3;
 constexpr uint32_t Q4K_A_SLAB = 64 * 128, Q4K_B_SLAB = 128 * 128;                      // bytes
 constexpr uint32_t Q4K_STAGE_BYTES = 2 * Q4K_A_SLAB + 2 * Q4K_B_SLAB;                 // 48 KB per 128-wide k-step
 constexpr uint32_t Q4K_RAW_BYTES = 128 * 144;                                          // one super-block per tile row
+// M = 64 instruction (the activation rows are the M operand and there are at most 64 of them): half the tensor-pipe time of the
+// M = 128 form.  Its accumulator sits in 16 lanes of each 32-lane quarter of tensor memory: row r in lane 32 (r / 16) + r % 16.
+constexpr uint32_t Q4K_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(GEMM_BN >> 3) << 17) | ((uint32_t)(64 >> 4) << 24);
 constexpr uint32_t Q4K_SMEM = Q4K_STAGES * Q4K_STAGE_BYTES + Q4K_RAW_STAGES * Q4K_RAW_BYTES + 1024 + 256;
 static_assert(Q4K_STAGES * Q4K_STAGE_BYTES >= GEMM_BM * GEMM_BN * 4, "the parked f32 tile reuses the stage buffers");
 
@@ -648,7 +651,7 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
                     const uint64_t adesc = make_smem_desc(a_addr + sl * Q4K_A_SLAB), bdesc = make_smem_desc(b_addr + sl * Q4K_B_SLAB);
 #pragma unroll
                     for (int k = 0; k < 4; ++k)
-                        umma_bf16(tmem_base, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), GEMM_IDESC, (i > 0 || sl > 0 || k > 0) ? 1u : 0u);
+                        umma_bf16(tmem_base, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), Q4K_IDESC, (i > 0 || sl > 0 || k > 0) ? 1u : 0u);
                 }
                 umma_commit(empty0 + 8 * st);
             }
@@ -729,20 +732,22 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
         if (warp < 6) {
             // ---- epilogue part 1: park the f32 tile column-major in the idle stage buffers ----
             const int q = warp & 3;
-            const int rloc = q * 32 + lane;
+            const int rloc = q * 16 + (lane & 15);                      // lanes 16-31 of a quarter hold nothing
             const bool ok = __all_sync(0xffffffffu, g_mbar_wait(tfull, 0, p.err, s_abort) && !*s_abort);
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             float* park = reinterpret_cast<float*>(tiles_ptr);          // [weight column of the tile][activation row]
 #pragma unroll
             for (int c = 0; c < GEMM_BN / 32; ++c) {
-                if (q * 32 >= p.M) break;                               // rows of this warp are never read back
+                if (q * 16 >= p.M) break;                               // rows of this warp are never read back
                 uint32_t v[32];
                 if (ok) {
                     tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 }
 #pragma unroll
-                for (int j = 0; j < 32; ++j) park[(c * 32 + j) * GEMM_BM + rloc] = ok ? __uint_as_float(v[j]) : 0.f;
+                if (lane < 16)
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) park[(c * 32 + j) * GEMM_BM + rloc] = ok ? __uint_as_float(v[j]) : 0.f;
             }
         }
     }
