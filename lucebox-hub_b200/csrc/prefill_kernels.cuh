@@ -534,7 +534,7 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
     }
 }
 
-// ---- scan over chunks: one CTA (8 compute warps + a copy warp) per (head, 16-wide slice of the value dimension) --------
+// ---- scan over chunks: one CTA (8 compute warps + a copy / MMA-issue warp) per (head, 16-wide slice of the value dimension) ----
 // Sequential over the chunks of a head; with S the state slice [128 k][16 v], per chunk
 //   W = w (k S),  v_new = vprime - T W,  out = d (q S) + aqk v_new,  S <- S exp(gc_last) + k^T (e v_new)
 // (w_i = beta_i exp(gc_i), d_i = exp(gc_i) / sqrt(128), e_i = exp(gc_last - gc_i); T W equals the chunk-64 formulation's
@@ -547,9 +547,12 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
 //   P1b T W and P2 aqk v_new (64 x 64 x 16, lower triangular, both operands f32) as 3xTF32 mma.sync tiles, the eight warps a
 //       4 x 2 grid of (16-token row tile, 8-column tile), zero k-steps skipped.
 // The state slice lives in registers from chunk to chunk, one row (key dim) of 8 columns per thread, as it comes out of
-// tensor memory; shared memory holds its three pieces as the right operand of the next chunk's P1.  The copy warp brings
-// each chunk's operands in with three bulk copies (completion counted on an mbarrier) into one of two stages, a chunk
-// ahead of the compute warps.  Row tiles of the last chunk that hold only padding are skipped.
+// tensor memory; shared memory holds its three pieces as the right operand of the next chunk's P1.  One lane of the ninth
+// warp brings each chunk's operands in with three bulk copies (completion counted on an mbarrier) into one of two stages, a
+// chunk ahead of the compute warps, and issues both tcgen05 products, each as soon as the compute warps have announced its
+// right operand on an mbarrier (state pieces -> P1, e v_new pieces -> P3).  P2 of a chunk is not on the path to the next
+// state: it runs under the next chunk's P1 (v_new and d (q S) are kept by chunk parity), and the chunk's stage is released
+// after it.  Row tiles of the last chunk that hold only padding are skipped.  Every wait is bounded and sets the status word.
 constexpr int SCAN_CONS = 256;              // compute threads
 constexpr int SCAN_THREADS = SCAN_CONS + 32;
 constexpr int SCAN_LDB = SCAN_VW + 4;       // W, v_new (hi and lo), d (q S): rows 2 t, 2 t + 1 of a k-step: bank = 8 t + g
