@@ -570,10 +570,15 @@ constexpr uint32_t SCAN_D2_COL = 64;        // first column of the second accumu
 constexpr uint32_t SCAN_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(SCAN_NB >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 constexpr unsigned SCAN_WAIT_LIMIT = 1u << 26;      // a bounded wait: a copy or an MMA that never completes ends the loop instead of hanging
 
+// (once the status word is set -- by this wait, by another thread's or by an earlier kernel -- every later wait gives up within
+// a thousand polls, so a failed pass ends quickly)
 __device__ __forceinline__ void scan_wait(uint32_t bar, uint32_t parity, int* err) {
     unsigned it = 0;
-    while (!mbar_try_wait(bar, parity))
-        if (++it >= SCAN_WAIT_LIMIT) { atomicCAS(err, 0, (int)ERR_BARRIER_TIMEOUT); return; }
+    while (!mbar_try_wait(bar, parity)) {
+        ++it;
+        if (it >= SCAN_WAIT_LIMIT) { atomicCAS(err, 0, (int)ERR_BARRIER_TIMEOUT); return; }
+        if ((it & 1023u) == 0 && *reinterpret_cast<volatile int*>(err) != 0) return;
+    }
 }
 __device__ __forceinline__ void scan_cons_sync() { asm volatile("bar.sync 1, %0;" ::"n"(SCAN_CONS) : "memory"); }
 // shared-memory matrix descriptor, K-major operand, 128-byte swizzle: start address >> 4 | SBO = 1024 B between 8-row groups |
