@@ -294,17 +294,19 @@ constexpr float CL_QSCALE = 0.08838834764831845f;        // 1 / sqrt(128)
 constexpr int CL_LD = DN_K + 4;                          // q, k: A operands (row-major) and, for k, the transposed B operand: bank = 4 g + t
 constexpr int CL_LDB = DN_K + 8;                         // v: B operand [token][dim]: bank = 8 t + g
 constexpr int CL_LDA = DN_CHUNK + 4;                     // T: A operand of the last product
-constexpr int CHUNK_LOCAL_SMEM = (2 * DN_CHUNK * CL_LD + DN_CHUNK * CL_LDB + 2 * DN_CHUNK * CL_LDA + 3 * 256 + 3 * DN_CHUNK) * 4;
+// q and v share one region (v replaces q once q k^T is done): 107 KB, so that two CTAs fit an SM and the phases of one
+// (loads, tensor-core products, the triangular solve on a few warps) run under those of the other
+constexpr int CHUNK_LOCAL_SMEM = (DN_CHUNK * CL_LD + DN_CHUNK * CL_LDB + 2 * DN_CHUNK * CL_LDA + 3 * 256 + 3 * DN_CHUNK) * 4;
 
-static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(const bf16* __restrict__ qkv, const float* __restrict__ beta,
+static __global__ void __launch_bounds__(CL_THREADS, 2) pf_dn_chunk_local_kernel(const bf16* __restrict__ qkv, const float* __restrict__ beta,
                                                                        const float* __restrict__ g, ChunkScratch* __restrict__ scratch,
                                                                        int S, int nchunks) {
     pdl_wait();
     extern __shared__ __align__(16) float sm[];
-    float* sq = sm;                                  // [64][CL_LD]   q / sqrt(128)
-    float* sk = sq + DN_CHUNK * CL_LD;               // [64][CL_LD]   k
-    float* sv = sk + DN_CHUNK * CL_LD;               // [64][CL_LDB]  v
-    float* sa = sv + DN_CHUNK * CL_LDB;              // [64][CL_LDA]  N = -(k beta) k^T * decay, strictly lower
+    float* sq = sm;                                  // [64][CL_LD]   q, until q k^T is done; then
+    float* sv = sm;                                  // [64][CL_LDB]  v (held in registers meanwhile)
+    float* sk = sm + DN_CHUNK * CL_LDB;              // [64][CL_LD]   k
+    float* sa = sk + DN_CHUNK * CL_LD;               // [64][CL_LDA]  N = -(k beta) k^T * decay, strictly lower
     float* sx = sa + DN_CHUNK * CL_LDA;              // [64][CL_LDA]  T = (I - N)^-1
     float* sw = sx + DN_CHUNK * CL_LDA;              // [3][16][16]   block products of the inversion
     float* sb = sw + 3 * 256;
@@ -320,7 +322,11 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
         sb[tid] = (t < S) ? beta[t * DN_HEADS + h] : 0.f;
         sg[tid] = (t < S) ? g[t * DN_HEADS + h] : 0.f;
     }
-    for (int e = tid; e < DN_CHUNK * (DN_K / 8); e += CL_THREADS) {          // eight dimensions (16 bytes of bf16) per step
+    static_assert(DN_CHUNK * (DN_K / 8) == 2 * CL_THREADS, "two 16-byte pieces of each of q, k, v per thread");
+    uint4 vreg[2];
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {                                          // eight dimensions (16 bytes of bf16) per step
+        const int e = tid + it * CL_THREADS;
         const int i = e >> 4, d = (e & 15) * 8, t = t0 + i;
         uint4 qr = make_uint4(0, 0, 0, 0), kr = qr, vr = qr;
         if (t < S) {
@@ -340,8 +346,7 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
         *reinterpret_cast<float4*>(sq + i * CL_LD + d + 4) = make_float4(bf_lo(qr.z), bf_hi(qr.z), bf_lo(qr.w), bf_hi(qr.w));
         *reinterpret_cast<float4*>(sk + i * CL_LD + d) = make_float4(bf_lo(kr.x), bf_hi(kr.x), bf_lo(kr.y), bf_hi(kr.y));
         *reinterpret_cast<float4*>(sk + i * CL_LD + d + 4) = make_float4(bf_lo(kr.z), bf_hi(kr.z), bf_lo(kr.w), bf_hi(kr.w));
-        *reinterpret_cast<float4*>(sv + i * CL_LDB + d) = make_float4(bf_lo(vr.x), bf_hi(vr.x), bf_lo(vr.y), bf_hi(vr.y));
-        *reinterpret_cast<float4*>(sv + i * CL_LDB + d + 4) = make_float4(bf_lo(vr.z), bf_hi(vr.z), bf_lo(vr.w), bf_hi(vr.w));
+        vreg[it] = vr;
     }
     __syncthreads();
     if (tid == 0) {                 // sequential cumsum, as torch.cumsum does
@@ -420,6 +425,15 @@ static __global__ void __launch_bounds__(CL_THREADS) pf_dn_chunk_local_kernel(co
         }
     }
     __syncthreads();
+    // q is no longer read: v takes its place (read by the last product, several barriers from here)
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+        const int e = tid + it * CL_THREADS;
+        const int i = e >> 4, d = (e & 15) * 8;
+        const uint4 vr = vreg[it];
+        *reinterpret_cast<float4*>(sv + i * CL_LDB + d) = make_float4(bf_lo(vr.x), bf_hi(vr.x), bf_lo(vr.y), bf_hi(vr.y));
+        *reinterpret_cast<float4*>(sv + i * CL_LDB + d + 4) = make_float4(bf_lo(vr.z), bf_hi(vr.z), bf_lo(vr.w), bf_hi(vr.w));
+    }
     // T = (I - N)^-1 with N = sa (strictly lower triangular), in 16 x 16 blocks.
     //   diagonal blocks: forward substitution inside the block (T_ij = N_ij + sum_{j < k < i} N_ik T_kj), one warp per block,
     //   one lane per column, so its 15 steps need no barrier at all;
