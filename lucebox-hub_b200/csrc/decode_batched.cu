@@ -614,7 +614,7 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
             Q35_CUDA_OK(pdl_launch(bd_dn_step_kernel, dim3(B, DN_HEADS, DN_V / BD_DN_ROWS), 256, 0, stream, proj, ldp, (const bf16*)L.p[DN_CONV], (const bf16*)L.p[DN_ALOG],
                                                                                   (const bf16*)L.p[DN_DTBIAS], conv, conv_stride, state, state_stride, core));
             Q35_CUDA_OK(pdl_launch(bd_conv_shift_kernel, (B * DN_CONV_CH + 255) / 256, 256, 0, stream, proj, ldp, conv, conv_stride, B));
-            Q35_CUDA_OK(pdl_launch(pf_gated_norm_kernel, (B * DN_HEADS + 7) / 8, 256, 0, stream, core, proj, ldp, (const bf16*)L.p[DN_NORM], attn, B));
+            Q35_CUDA_OK(pdl_launch(pf_gated_norm_kernel, (B * DN_HEADS + 15) / 16, 256, 0, stream, core, proj, ldp, (const bf16*)L.p[DN_NORM], attn, B));
             g_launches.fetch_add(3);
             w_out = (const bf16*)L.p[DN_OUT]; w_post = (const bf16*)L.p[DN_POST_NORM]; w_down = (const bf16*)L.p[DN_DOWN];
             ++i_dn;

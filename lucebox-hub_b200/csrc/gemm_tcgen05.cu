@@ -896,6 +896,25 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
     void* ws = get_workspace();
     if (!ws) return QWEN35_ERR_CUDA;
     if (epi < 0 || epi > 2) { set_error("gemm_bf16: unknown epilogue %d", epi); return QWEN35_ERR_BAD_ARG; }
+    // Many rows of 256-column tiles whose count is a little above a whole number of waves (296 tiles, two CTAs per SM): the
+    // last, nearly empty wave costs as much as a full one.  The rows of tiles that spill over are split off into a call of
+    // their own (the 4096 x 7168 gate/up GEMM: 896 tiles = 3 waves + 8 tiles; 31 rows of tiles fill 2.93 waves, the 32nd runs
+    // as a 128-row problem behind them).
+    {
+        const int mt = (M + GEMM_BM - 1) / GEMM_BM;
+        const int ntw = (N + ((epi == EPI_SILU_MUL) ? GEMM_BN_WIDE / 2 : GEMM_BN_WIDE) - 1) / ((epi == EPI_SILU_MUL) ? GEMM_BN_WIDE / 2 : GEMM_BN_WIDE);
+        const int over = (mt * ntw) % 296;
+        if (epi != EPI_RESIDUAL && mt >= 9 && mt * ntw > 296 && over > 0 && over <= 45) {
+            const int peel = (over + ntw - 1) / ntw;
+            if (peel * 4 <= mt) {
+                const int m_main = (mt - peel) * GEMM_BM;
+                const int st0 = gemm_bf16(A, lda, B, b_rows, C, ldc, R, ldr, m_main, N, K, epi, up_row_offset, stream);
+                if (st0 != QWEN35_OK) return st0;
+                return gemm_bf16(A + (size_t)m_main * lda, lda, B, b_rows, C + (size_t)m_main * ldc, ldc, R ? R + (size_t)m_main * ldr : nullptr, ldr,
+                                 M - m_main, N, K, epi, up_row_offset, stream);
+            }
+        }
+    }
     GemmParams p{M, N, K, C, ldc, R, ldr, up_row_offset, (int*)ws};
     const int nkb = K / GEMM_BK;
     const int m_tiles = (M + GEMM_BM - 1) / GEMM_BM;

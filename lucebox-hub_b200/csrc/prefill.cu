@@ -134,7 +134,7 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
             Q35_CUDA_OK(pdl_launch(pf_dn_chunk_local_kernel, dim3(nchunks, DN_HEADS), CL_THREADS, CHUNK_LOCAL_SMEM, stream, a.proj_buf2, a.beta_buf, a.alpha_buf, scratch, S, nchunks));
             Q35_CUDA_OK(pdl_launch(pf_dn_chunk_scan_kernel, dim3(DN_HEADS, DN_V / SCAN_VW), SCAN_THREADS, CHUNK_SCAN_SMEM, stream, 
                 scratch, a.dn_out_buf, a.dn_states + (size_t)i_dn * DN_HEADS * DN_V * DN_K, S, nchunks, err_word));
-            Q35_CUDA_OK(pdl_launch(pf_gated_norm_kernel, (S * DN_HEADS + 7) / 8, 256, 0, stream, a.dn_out_buf, a.proj_buf, ldp, (const bf16*)L.p[DN_NORM], a.attn_buf, S));
+            Q35_CUDA_OK(pdl_launch(pf_gated_norm_kernel, (S * DN_HEADS + 15) / 16, 256, 0, stream, a.dn_out_buf, a.proj_buf, ldp, (const bf16*)L.p[DN_NORM], a.attn_buf, S));
             g_launches.fetch_add(4);
             w_out = (const bf16*)L.p[DN_OUT]; w_post = (const bf16*)L.p[DN_POST_NORM]; w_down = (const bf16*)L.p[DN_DOWN];
             ++i_dn;

@@ -890,27 +890,37 @@ static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(c
     }
 }
 
-// ---- gated RMSNorm of the DeltaNet output: one warp per (token, head) --------------------------------
+// ---- gated RMSNorm of the DeltaNet output: half a warp per (token, head) -----------------------------
 static __global__ void __launch_bounds__(256) pf_gated_norm_kernel(const bf16* __restrict__ core, const bf16* __restrict__ proj, int ldp,
                                                             const bf16* __restrict__ norm_w, bf16* __restrict__ out, int S) {
     pdl_wait();
-    const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (gw >= S * DN_HEADS) return;
-    const int t = gw / DN_HEADS, h = gw % DN_HEADS;
-    const uint2 orw = *(reinterpret_cast<const uint2*>(core + (size_t)t * DN_V_SIZE + h * DN_V) + lane);
-    const uint2 zrw = *(reinterpret_cast<const uint2*>(proj + (size_t)t * ldp + DN_CONV_CH + h * DN_V) + lane);
-    const uint2 nrw = __ldg(reinterpret_cast<const uint2*>(norm_w) + lane);
-    const float ov[4] = {bf_lo(orw.x), bf_hi(orw.x), bf_lo(orw.y), bf_hi(orw.y)};
-    const float zv[4] = {bf_lo(zrw.x), bf_hi(zrw.x), bf_lo(zrw.y), bf_hi(zrw.y)};
-    const float nw[4] = {bf_lo(nrw.x), bf_hi(nrw.x), bf_lo(nrw.y), bf_hi(nrw.y)};
-    const float var = warp_sum(ov[0] * ov[0] + ov[1] * ov[1] + ov[2] * ov[2] + ov[3] * ov[3]) * (1.0f / DN_V);
-    const float r = rsqrt_ieee(var + RMS_EPS);
-    float u[4];
+    // half a warp per (token, head): 16 lanes x 8 values, 16-byte loads and stores
+    const int lane = threadIdx.x & 31, l16 = lane & 15;
+    const int gw = (blockIdx.x * 8 + (threadIdx.x >> 5)) * 2 + (lane >> 4);
+    const bool live = gw < S * DN_HEADS;
+    const int t = live ? gw / DN_HEADS : 0, h = live ? gw % DN_HEADS : 0;
+    uint4 orw = make_uint4(0, 0, 0, 0), zrw = orw;
+    if (live) {
+        orw = *(reinterpret_cast<const uint4*>(core + (size_t)t * DN_V_SIZE + h * DN_V) + l16);
+        zrw = *(reinterpret_cast<const uint4*>(proj + (size_t)t * ldp + DN_CONV_CH + h * DN_V) + l16);
+    }
+    const uint4 nrw = __ldg(reinterpret_cast<const uint4*>(norm_w) + l16);
+    const uint32_t ow[4] = {orw.x, orw.y, orw.z, orw.w}, zw[4] = {zrw.x, zrw.y, zrw.z, zrw.w}, nwd[4] = {nrw.x, nrw.y, nrw.z, nrw.w};
+    float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) u[i] = rbf(nw[i] * rbf(ov[i] * r)) * silu_f(zv[i]);
-    bf16* dst = out + (size_t)t * DN_V_SIZE + h * DN_V + lane * 4;
-    *reinterpret_cast<__nv_bfloat162*>(dst) = __halves2bfloat162(f2bf(u[0]), f2bf(u[1]));
-    *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __halves2bfloat162(f2bf(u[2]), f2bf(u[3]));
+    for (int i = 0; i < 4; ++i) ss += bf_lo(ow[i]) * bf_lo(ow[i]) + bf_hi(ow[i]) * bf_hi(ow[i]);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);          // within the half warp
+    const float r = rsqrt_ieee(ss * (1.0f / DN_V) + RMS_EPS);
+    uint32_t res[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float u0 = rbf(bf_lo(nwd[i]) * rbf(bf_lo(ow[i]) * r)) * silu_f(bf_lo(zw[i]));
+        const float u1 = rbf(bf_hi(nwd[i]) * rbf(bf_hi(ow[i]) * r)) * silu_f(bf_hi(zw[i]));
+        const __nv_bfloat162 pr = __halves2bfloat162(f2bf(u0), f2bf(u1));
+        res[i] = *reinterpret_cast<const uint32_t*>(&pr);
+    }
+    if (live) *(reinterpret_cast<uint4*>(out + (size_t)t * DN_V_SIZE + h * DN_V) + l16) = make_uint4(res[0], res[1], res[2], res[3]);
 }
 
 // ---- attention preparation: one warp per (token, head slot); slots 0-7 query heads, 8-9 key heads, 10-11 value heads

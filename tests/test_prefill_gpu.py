@@ -71,7 +71,7 @@ def test_gemm_fused_epilogues():
     got = _gemm(A, B, N, epi=1, R=R)
     ref = (A.float() @ B.float().t()).bfloat16() + R
     assert float((got != ref).float().mean()) <= GEMM_FLIP_FRAC
-    for M, N, K in ((130, 3584, 1024), (64, 3584, 1024), (64, 520, 1024), (16, 40, 128), (2048, 3584, 1024), (1900, 3600, 128)):
+    for M, N, K in ((130, 3584, 1024), (64, 3584, 1024), (64, 520, 1024), (16, 40, 128), (2048, 3584, 1024), (1900, 3600, 128), (4096, 3584, 1024)):
         A = torch.randn(M, K, device="cuda").bfloat16()
         B = (torch.randn(2 * N, K, device="cuda") * 0.05).bfloat16()
         got = _gemm(A, B, N, epi=2, up_off=N)
