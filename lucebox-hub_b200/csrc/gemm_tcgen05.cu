@@ -38,8 +38,8 @@ constexpr int GEMM_BN_NARROW = 64, GEMM_STAGES_NARROW = 8, GEMM_STAGES_NARROW_SP
 // The epilogue parks the f32 accumulator tile in the (then idle) stage buffers as [row][GEMM_PARK_LD]: with a pitch of
 // 132 floats the float4 accesses of eight adjacent rows (writing, one row per thread) and of one row's adjacent column
 // groups (reading) both spread over all 32 banks.
-// The 256-column tile of the many-wave problems applies its epilogue arithmetic on the way out of tensor memory and parks
-// bf16 [row][GEMM_PARK_LD_WIDE] (a pitch of 132 words: the 16-byte stores of eight adjacent rows cover all 32 banks).
+// The 256-column tile of the many-wave problems parks its accumulator rounded to bf16, [row][GEMM_PARK_LD_WIDE] (a pitch of
+// 132 words: the 16-byte stores of eight adjacent rows cover all 32 banks); residual or SiLU * up are applied by the store pass.
 constexpr int GEMM_BN_WIDE = 256, GEMM_STAGES_WIDE_TILE = 2, GEMM_PARK_LD_WIDE = GEMM_BN_WIDE + 8;
 __host__ __device__ constexpr uint32_t gemm_park_bytes(int bn) {
     return bn == GEMM_BN_WIDE ? (uint32_t)GEMM_BM * GEMM_PARK_LD_WIDE * 2 : (uint32_t)GEMM_BM * (bn + 4) * 4;
@@ -303,7 +303,18 @@ __device__ __forceinline__ void parked_tile_store_wide(const GemmParams& p, cons
     const bool vec_ok = n0 + col + 8 <= p.N && ((reinterpret_cast<uintptr_t>(p.C + n0 + col) | (size_t)p.ldc * 2) & 15) == 0 &&
                         (EPI != EPI_RESIDUAL || ((reinterpret_cast<uintptr_t>(p.R + n0 + col) | (size_t)p.ldr * 2) & 15) == 0);
     for (int r = r_first; r < rows; r += r_step) {
-        const uint4 v = *reinterpret_cast<const uint4*>(park + (size_t)r * GEMM_PARK_LD_WIDE + col);
+        uint4 v = *reinterpret_cast<const uint4*>(park + (size_t)r * GEMM_PARK_LD_WIDE + col);
+        if (EPI == EPI_SILU_MUL) {              // gate columns [0, 128), up columns [128, 256) of the parked row, both bf16 already
+            const uint4 u = *reinterpret_cast<const uint4*>(park + (size_t)r * GEMM_PARK_LD_WIDE + GEMM_BN_WIDE / 2 + col);
+            const uint32_t g4[4] = {v.x, v.y, v.z, v.w}, u4[4] = {u.x, u.y, u.z, u.w};
+            uint32_t y4[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const __nv_bfloat162 pr = __halves2bfloat162(f2bf(rbf(silu_f(bf_lo(g4[j]))) * bf_lo(u4[j])), f2bf(rbf(silu_f(bf_hi(g4[j]))) * bf_hi(u4[j])));
+                y4[j] = *reinterpret_cast<const uint32_t*>(&pr);
+            }
+            v = make_uint4(y4[0], y4[1], y4[2], y4[3]);
+        }
         if (vec_ok) {
             uint4 o = v;
             if (EPI == EPI_RESIDUAL) {
@@ -422,15 +433,14 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
         const bool ok = __all_sync(0xffffffffu, g_mbar_wait(tfull, 0, p.err, s_abort) && !*s_abort);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         if (BN == GEMM_BN_WIDE) {
-            // 256-column tile: epilogue arithmetic here (a thread holds its row), results parked as bf16 for the store pass
+            // 256-column tile: the accumulator rows are rounded to bf16 and parked; the store pass (all six warps) does the rest
             bf16* parkh = reinterpret_cast<bf16*>(tiles_ptr) + (size_t)rloc * GEMM_PARK_LD_WIDE;
             if (m0 + q * 32 < p.M) {
 #pragma unroll 1
-                for (int c = 0; c < BN_OUT / 32; ++c) {
-                    uint32_t v[32], w[32];
+                for (int c = 0; c < BN / 32; ++c) {
+                    uint32_t v[32];
                     if (ok) {
                         tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
-                        if (EPI == EPI_SILU_MUL) tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(BN / 2 + c * 32), w);
                         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                     }
 #pragma unroll
@@ -438,15 +448,7 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
                         uint32_t o[4];
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            float y0 = 0.f, y1 = 0.f;
-                            if (ok) {
-                                const float g0 = __uint_as_float(v[j + 2 * e]), g1 = __uint_as_float(v[j + 2 * e + 1]);
-                                if (EPI == EPI_SILU_MUL) {
-                                    y0 = rbf(silu_f(rbf(g0))) * rbf(__uint_as_float(w[j + 2 * e]));
-                                    y1 = rbf(silu_f(rbf(g1))) * rbf(__uint_as_float(w[j + 2 * e + 1]));
-                                } else { y0 = g0; y1 = g1; }
-                            }
-                            const __nv_bfloat162 pr = __halves2bfloat162(f2bf(y0), f2bf(y1));
+                            const __nv_bfloat162 pr = __halves2bfloat162(f2bf(ok ? __uint_as_float(v[j + 2 * e]) : 0.f), f2bf(ok ? __uint_as_float(v[j + 2 * e + 1]) : 0.f));
                             o[e] = *reinterpret_cast<const uint32_t*>(&pr);
                         }
                         *reinterpret_cast<uint4*>(parkh + c * 32 + j) = make_uint4(o[0], o[1], o[2], o[3]);
