@@ -951,10 +951,11 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
     const int bn_out_wd = (epi == EPI_SILU_MUL) ? GEMM_BN_WIDE / 2 : GEMM_BN_WIDE;
     const int nt_wd = (N + bn_out_wd - 1) / bn_out_wd;
     // Taken from 8 rows of tiles on, when its waves (two CTAs per SM) cost less than the 128-column tile's: a wave of the wide
-    // tile takes 1.8 x as long for twice the work (measured at 4096 x 8224 x 1024), and either form pays for a whole last wave.
+    // tile takes 1.5-1.8 x as long for twice the work (measured at 4096 x 8224 x 1024 and 4096 x 7168 x 1024; the factor 1.5 was the
+    // best of 1.2 / 1.5 / 1.8 over prompts of 1024 to 4096 tokens), and either form pays for a whole last wave.
     const int slots_n = tiles_total <= 148 ? 148 : (tiles_total > 296 && tiles_total <= 444) ? 444 : 296;
     const int waves_n = (tiles_total + slots_n - 1) / slots_n, waves_wd = (m_tiles * nt_wd + 295) / 296;
-    const bool wide_tile = !narrow && epi != EPI_RESIDUAL && m_tiles >= 8 && 18 * waves_wd < 10 * waves_n;
+    const bool wide_tile = !narrow && epi != EPI_RESIDUAL && m_tiles >= 8 && 15 * waves_wd < 10 * waves_n;
     const int b_box = wide_tile ? 128 : !narrow ? 64 : (epi == EPI_SILU_MUL ? GEMM_BN_NARROW / 2 : GEMM_BN_NARROW);
     if (!make_tmap(&tmA, A, M, K, lda, GEMM_BM) || !make_tmap(&tmB, B, b_rows, K, K, b_box)) {
         set_error("cuTensorMapEncodeTiled failed (A %p [%d x %d] ld %d; B %p [%d x %d])", (const void*)A, M, K, lda, (const void*)B, b_rows, K);
