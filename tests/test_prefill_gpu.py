@@ -47,10 +47,10 @@ def _gemm(A, B, N, epi=0, R=None, up_off=0):
 
 
 # single-row-of-tiles shapes (M <= 128) run the narrow 64-column tiles, the last three (8 or more rows of tiles, fewer waves that way) the
-# 128 x 256 tile, the others the 128-column tile
+# 128 x 256 tile (the last one with its 30th row of tiles split off into a call of its own), the others the 128-column tile
 @pytest.mark.parametrize("M,N,K", [(1, 64, 64), (7, 96, 128), (128, 128, 1024), (520, 8224, 1024), (333, 1024, 3584), (1024, 5120, 1024),
                                    (64, 1024, 2048), (64, 5120, 1024), (64, 8224, 1024), (33, 1000, 3584), (128, 20000, 1024),
-                                   (1990, 8224, 1024), (4096, 5120, 2048), (3000, 4100, 64)])
+                                   (1990, 8224, 1024), (4096, 5120, 2048), (3000, 4100, 64), (3840, 2560, 256)])
 def test_gemm_plain(M, N, K):
     torch.manual_seed(M * 7 + N)
     A = torch.randn(M, K, device="cuda").bfloat16()
