@@ -46,7 +46,7 @@ def _gemm(A, B, N, epi=0, R=None, up_off=0):
     return out
 
 
-# single-row-of-tiles shapes (M <= 128) run the narrow 64-column tiles, the last three (8 or more rows of tiles, fewer waves that way) the
+# single-row-of-tiles shapes (M <= 128) run the narrow 64-column tiles, the last four (8 or more rows of tiles, fewer waves that way) the
 # 128 x 256 tile (the last one with its 30th row of tiles split off into a call of its own), the others the 128-column tile
 @pytest.mark.parametrize("M,N,K", [(1, 64, 64), (7, 96, 128), (128, 128, 1024), (520, 8224, 1024), (333, 1024, 3584), (1024, 5120, 1024),
                                    (64, 1024, 2048), (64, 5120, 1024), (64, 8224, 1024), (33, 1000, 3584), (128, 20000, 1024),
