@@ -116,6 +116,18 @@ __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint6
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
         ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
 }
+// A operand in tensor memory (128 lanes = rows, one 32-bit column per two bf16 of K), B operand in shared memory
+__device__ __forceinline__ void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate) : "memory");
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+                 ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]) : "memory");
+}
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
@@ -184,7 +196,7 @@ __device__ __forceinline__ void epilogue_store8(const GemmParams& p, int row, in
 // shared-memory offset; CTA `rank` finishes columns [rank * BN_OUT / S, +BN_OUT / S) for `rows` rows.  A work item is one
 // row x 8 adjacent columns: all peers' values are requested before the first is used (one remote round trip, not S), then
 // summed in peer order, so the result does not depend on timing.  `t` is the calling thread's index among `nt` workers.
-template <int EPI, int BN = GEMM_BN>
+template <int EPI, int BN = GEMM_BN, bool ROT = false>
 __device__ __forceinline__ void cluster_reduce_store(const GemmParams& p, uint32_t park_local, int S, int rows, int m0, int n0, int t, int nt) {
     constexpr int BN_OUT = (EPI == EPI_SILU_MUL) ? BN / 2 : BN;
     const uint32_t rank = cluster_ctarank();
@@ -199,7 +211,7 @@ __device__ __forceinline__ void cluster_reduce_store(const GemmParams& p, uint32
             if (peer < S) {
                 const uint32_t base = map_to_cta(park_local, (uint32_t)peer);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) v[peer][e] = ld_dsmem(base + (uint32_t)(((col + e) * GEMM_BM + r) * 4));
+                for (int e = 0; e < 8; ++e) v[peer][e] = ld_dsmem(base + (uint32_t)(((col + e) * GEMM_BM + (ROT ? ((r + col + e) & 63) : r)) * 4));
             }
 #pragma unroll
         for (int e = 0; e < 8; ++e) { g[e] = 0.f; u[e] = 0.f; }
@@ -215,7 +227,8 @@ __device__ __forceinline__ void cluster_reduce_store(const GemmParams& p, uint32
                 if (peer < S) {
                     const uint32_t base = map_to_cta(park_local, (uint32_t)peer);
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) v[peer][e] = ld_dsmem(base + (uint32_t)(((BN / 2 + col + e) * GEMM_BM + r) * 4));
+                    for (int e = 0; e < 8; ++e)
+                        v[peer][e] = ld_dsmem(base + (uint32_t)(((BN / 2 + col + e) * GEMM_BM + (ROT ? ((r + BN / 2 + col + e) & 63) : r)) * 4));
                 }
 #pragma unroll
             for (int peer = 0; peer < GEMM_MAX_SPLIT; ++peer)
@@ -509,34 +522,36 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
 
 // ------------------------------------------------------------------------------------------------------------
 // Q4_K weights: C[M <= 64, N] = epi(A[M, K] . dequant(W[N, K])^T).  Same split-K cluster scheme as above, but the
-// weight operand never exists in global memory as bf16:
-//   warp 0      TMA producer of the activation tiles (two 64-wide slabs per 128-wide k-step)
+// weight operand never exists as bf16 in global OR shared memory: the dequantised tile goes straight into tensor memory
+// and is the MMA's A operand (128 weight rows = 128 lanes; the activation rows are the N dimension, read from shared
+// memory).  The form before this one wrote the bf16 tile into shared memory for the MMA to read back: its counters
+// showed the shared-memory data pipe full in the main loop (1 060 wavefronts per k-step = the k-step's cycles: 362
+// tile stores, 384 MMA operand reads, 115 raw loads, 200 of TMA writes); this form needs about 440.
+//   warp 0      TMA producer of the activation tiles (two 64-wide slabs per 128-wide k-step, 64 token rows each)
 //   warp 18     TMA producer of the RAW Q4_K super-blocks, one box of 144 bytes x 64 rows per half tile (a whole
 //               super-block row per request: HBM sees contiguous 144-byte pieces, never 16- or 32-byte ones); its own
 //               warp so that the raw ring runs its full depth ahead of the dequantisation
-//   warps 2-17  dequantise from the raw ring into the 128-byte-swizzled bf16 tile the MMA descriptor expects:
-//               a 64-weight group of a super-block is exactly one 64-wide slab row, so thread (row, h) converts
-//               group h of the k-step for one tile row (3 conflict-free 16-byte shared loads, 8 swizzled stores)
-//   warp 1      MMA issue: 8 x (M128 N128 K16) per k-step once both operands of the stage are there
-//   warps 2-5   epilogue afterwards (park, cluster reduce, store) as in the bf16 kernel
-// The activation box holds 64 rows; the MMA reads 128, so accumulator rows 64-127 are garbage and are never read.
-// ncu on a full wave of the gate/up widths (33 x 9472 x 5120): tensor pipe 33 % active, issue slots 47 % busy, 4.9
-// instructions per weight, HBM 19 %: the kernel is bound by the dequantisation arithmetic, not by HBM or the MMA.
+//   warps 2-17  dequantise from the raw ring into tensor memory: warp w owns the lanes 32 (w % 4) .. + 31 (the only ones
+//               it may touch), thread = one weight row; per k-step it converts 32 weights (two 8-column tcgen05.st)
+//   warp 1      MMA issue: 8 x (M128 N<=64 K16) per k-step once both operands of the stage are there
+//   warps 2-5   epilogue afterwards (park, cluster reduce, store); the accumulator is [weight row][token]
 // The weight operand is value = fma_bf16(q, bf16(d*sc), -bf16(dmin*m)), two weights per instruction: the published f32
-// dequantisation (d*sc)*q - dmin*m followed by a rounding to bf16 cost ~10 instructions per weight on the CUDA cores
-// and bounded the kernel harder still.  qwen35_b200_dequant_q4k keeps the published arithmetic bit for bit.  (An f16 weight
-// operand beside bf16 activations is not an option: kind::f16 with different A and B formats raised "illegal
-// instruction" on this GPU.)
+// dequantisation (d*sc)*q - dmin*m followed by a rounding to bf16 cost ~10 instructions per weight on the CUDA cores.
+// qwen35_b200_dequant_q4k keeps the published arithmetic bit for bit.  (An f16 weight operand beside bf16 activations
+// is not an option: kind::f16 with different A and B formats raised "illegal instruction" on this GPU.)
 constexpr int Q4K_THREADS = 608;                                                      // 2 + 16 dequantisation warps + the raw producer
 constexpr int Q4K_DQ_WARPS = 16;
 constexpr int Q4K_RAW_WARP = 2 + Q4K_DQ_WARPS;
-constexpr int Q4K_STAGES = 3, Q4K_RAW_STAGES = 3;
-constexpr uint32_t Q4K_A_SLAB = 64 * 128, Q4K_B_SLAB = 128 * 128;                      // bytes
-constexpr uint32_t Q4K_STAGE_BYTES = 2 * Q4K_A_SLAB + 2 * Q4K_B_SLAB;                 // 48 KB per 128-wide k-step
+constexpr int Q4K_STAGES = 4, Q4K_RAW_STAGES = 3;
+constexpr uint32_t Q4K_X_SLAB = 64 * 128;                                              // bytes: 64 token rows x 64 k
+constexpr uint32_t Q4K_STAGE_BYTES = 2 * Q4K_X_SLAB;                                  // 16 KB of activations per 128-wide k-step
 constexpr uint32_t Q4K_RAW_BYTES = 128 * 144;                                          // one super-block per tile row
-// M = 64 instruction (the activation rows are the M operand and there are at most 64 of them): half the tensor-pipe time of the
-// M = 128 form.  Its accumulator sits in 16 lanes of each 32-lane quarter of tensor memory: row r in lane 32 (r / 16) + r % 16.
-constexpr uint32_t Q4K_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(GEMM_BN >> 3) << 17) | ((uint32_t)(64 >> 4) << 24);
+// tensor memory: per stage 64 columns of weights (128 k as bf16 pairs), then the f32 accumulator [128 weights][64 tokens]
+constexpr uint32_t Q4K_W_COLS = 64, Q4K_D_COL = Q4K_STAGES * Q4K_W_COLS, Q4K_TMEM_COLS = 512;
+static_assert(Q4K_D_COL + 64 <= Q4K_TMEM_COLS, "tensor memory budget");
+__device__ __forceinline__ uint32_t q4k_idesc(int n_tokens) {      // D f32, A and B bf16, M = 128 weight rows, N = tokens rounded up to 16
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n_tokens >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
 constexpr uint32_t Q4K_SMEM = Q4K_STAGES * Q4K_STAGE_BYTES + Q4K_RAW_STAGES * Q4K_RAW_BYTES + 1024 + 256;
 static_assert(Q4K_STAGES * Q4K_STAGE_BYTES >= GEMM_BM * GEMM_BN * 4, "the parked f32 tile reuses the stage buffers");
 
@@ -587,7 +602,7 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(g_smem_u32(tmem_slot)), "r"(128u) : "memory");
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(g_smem_u32(tmem_slot)), "r"(Q4K_TMEM_COLS) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -603,11 +618,11 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
             for (int i = 0; i < nk2; ++i) {
                 const int st = i % STAGES;
                 if (!g_mbar_wait(empty0 + 8 * st, ((i / STAGES) & 1) ^ 1, p.err, s_abort)) break;
-                g_mbar_expect_tx(fulla0 + 8 * st, 2 * Q4K_A_SLAB);
+                g_mbar_expect_tx(fulla0 + 8 * st, 2 * Q4K_X_SLAB);
                 const uint32_t a_dst = tiles + st * Q4K_STAGE_BYTES;
                 const int kcol = (sb_begin * 2 + i) * 128;
                 g_tma_load_2d(a_dst, &tmA, kcol, 0, fulla0 + 8 * st);
-                g_tma_load_2d(a_dst + Q4K_A_SLAB, &tmA, kcol + 64, 0, fulla0 + 8 * st);
+                g_tma_load_2d(a_dst + Q4K_X_SLAB, &tmA, kcol + 64, 0, fulla0 + 8 * st);
                 issued_a = i + 1;
             }
             if (*s_abort) {      // copies in flight must land before the CTA may exit
@@ -642,18 +657,20 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
         }
     } else if (warp == 1) {
         if (lane == 0) {
+            const uint32_t idesc = q4k_idesc(min(64, max(16, (p.M + 15) & ~15)));
             for (int i = 0; i < nk2; ++i) {
                 const int st = i % STAGES;
                 if (!g_mbar_wait(fulla0 + 8 * st, (i / STAGES) & 1, p.err, s_abort)) break;
                 if (!g_mbar_wait(fullb0 + 8 * st, (i / STAGES) & 1, p.err, s_abort)) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t a_addr = tiles + st * Q4K_STAGE_BYTES, b_addr = a_addr + 2 * Q4K_A_SLAB;
+                const uint32_t x_addr = tiles + st * Q4K_STAGE_BYTES, w_col = tmem_base + (uint32_t)st * Q4K_W_COLS;
 #pragma unroll
                 for (int sl = 0; sl < 2; ++sl) {
-                    const uint64_t adesc = make_smem_desc(a_addr + sl * Q4K_A_SLAB), bdesc = make_smem_desc(b_addr + sl * Q4K_B_SLAB);
+                    const uint64_t xdesc = make_smem_desc(x_addr + sl * Q4K_X_SLAB);
 #pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        umma_bf16(tmem_base, adesc + (uint64_t)(2 * k), bdesc + (uint64_t)(2 * k), Q4K_IDESC, (i > 0 || sl > 0 || k > 0) ? 1u : 0u);
+                    for (int k = 0; k < 4; ++k)      // 16 k = 8 columns of the weight operand, 32 bytes of the activation rows
+                        umma_bf16_ts(tmem_base + Q4K_D_COL, w_col + (uint32_t)(sl * 32 + k * 8), xdesc + (uint64_t)(2 * k), idesc,
+                                     (i > 0 || sl > 0 || k > 0) ? 1u : 0u);
                 }
                 umma_commit(empty0 + 8 * st);
             }
@@ -664,12 +681,10 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
         // (16 nibble bytes = 32 weights: chunks 2*part, 2*part+1 from the low nibbles, 4+2*part, 5+2*part from the high
         // ones).  The loop runs per super-block with the k-step parity known at compile time: the 6-bit scale decoding
         // is branch-free, the header is read once for both k-steps, and ring positions advance by counters. ----
-        const int dw = warp - 2, row = (dw & 3) * 32 + lane, h = (dw >> 2) & 1, part = dw >> 3;
+        const int dw = warp - 2, row = (warp & 3) * 32 + lane, h = (dw >> 2) & 1, part = dw >> 3;
         const int sh = 16 * h;
-        uint32_t off[4];
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) off[cc] = (uint32_t)(((((cc >= 2) ? 4 : 0) + 2 * part + (cc & 1)) ^ (row & 7)) << 4);
-        unsigned char* const bbase = tiles_ptr + 2 * Q4K_A_SLAB + h * Q4K_B_SLAB + row * 128;
+        // this thread's 32 weights of a k-step: k = 64 h + 16 part + 0..15 (low nibbles) and 64 h + 32 + 16 part + 0..15 (high)
+        const uint32_t wdst = tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(32 * h + 8 * part);
         const unsigned char* const rbase = rawring_ptr + row * 144;
         const __nv_bfloat162 k128 = __float2bfloat162_rn(128.0f);
         int st = 0, rs = 0;
@@ -701,16 +716,14 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
                 const __nv_bfloat162 ds0 = __float2bfloat162_rn(__fmul_rn(d, (float)sc0)), ds1 = __float2bfloat162_rn(__fmul_rn(d, (float)sc1));
                 const __nv_bfloat162 nm0 = __float2bfloat162_rn(__fmul_rn(ndmin, (float)mn0)), nm1 = __float2bfloat162_rn(__fmul_rn(ndmin, (float)mn1));
                 const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
-                unsigned char* brow = bbase + st * Q4K_STAGE_BYTES;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");   // the MMAs that read this stage are done
 #pragma unroll
-                for (int cc = 0; cc < 4; ++cc) {                    // cc 0,1: low nibbles; 2,3: high nibbles
-                    const bool hi = cc >= 2;
+                for (int hi = 0; hi < 2; ++hi) {                    // 16 weights from the low nibbles, then 16 from the high ones
                     const __nv_bfloat162 dsx = hi ? ds1 : ds0, nmx = hi ? nm1 : nm0;
-                    uint32_t o[4];
+                    uint32_t o[8];
 #pragma unroll
-                    for (int h2 = 0; h2 < 2; ++h2) {
-                        const uint32_t word = w[2 * (cc & 1) + h2];
-                        const uint32_t nib = (hi ? (word >> 4) : word) & 0x0F0F0F0Fu;
+                    for (int h2 = 0; h2 < 4; ++h2) {
+                        const uint32_t nib = (hi ? (w[h2] >> 4) : w[h2]) & 0x0F0F0F0Fu;
                         // bytes (q, 0x43) are the bf16 numbers 128 + q: exact, no integer conversion
                         const uint32_t u01 = __byte_perm(nib, 0x43004300u, 0x7150), u23 = __byte_perm(nib, 0x43004300u, 0x7352);
                         const __nv_bfloat162 x01 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&u01), k128);
@@ -719,9 +732,10 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
                         o[2 * h2] = *reinterpret_cast<const uint32_t*>(&y01);
                         o[2 * h2 + 1] = *reinterpret_cast<const uint32_t*>(&y23);
                     }
-                    *reinterpret_cast<uint4*>(brow + off[cc]) = make_uint4(o[0], o[1], o[2], o[3]);
+                    tmem_st8(wdst + (uint32_t)(st * (int)Q4K_W_COLS + 16 * hi), o);     // columns = k / 2, the pair's first weight in the low half
                 }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");      // generic-proxy writes -> visible to the MMA
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) {
                     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(fullb0 + 8 * st) : "memory");
@@ -733,36 +747,35 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
         }
         if (warp < 6) {
             // ---- epilogue part 1: park the f32 tile column-major in the idle stage buffers ----
-            const int q = warp & 3;
-            const int rloc = q * 16 + (lane & 15);                      // lanes 16-31 of a quarter hold nothing
+            const int wrow = (warp & 3) * 32 + lane;                    // this thread's weight row = its tensor-memory lane
             const bool ok = __all_sync(0xffffffffu, g_mbar_wait(tfull, 0, p.err, s_abort) && !*s_abort);
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            float* park = reinterpret_cast<float*>(tiles_ptr);          // [weight column of the tile][activation row]
+            // [weight row of the tile][token], the tokens of row w rotated by w so that a warp's stores (32 rows, one token)
+            // fall into 32 different banks; cluster_reduce_store<.., true> undoes the rotation
+            float* park = reinterpret_cast<float*>(tiles_ptr) + wrow * GEMM_BM;
 #pragma unroll
-            for (int c = 0; c < GEMM_BN / 32; ++c) {
-                if (q * 16 >= p.M) break;                               // rows of this warp are never read back
+            for (int c = 0; c < 2; ++c) {
+                if (c * 32 >= p.M) break;                               // tokens that do not exist are never read back
                 uint32_t v[32];
                 if (ok) {
-                    tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 32), v);
+                    tmem_ld32(tmem_base + Q4K_D_COL + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(c * 32), v);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 }
 #pragma unroll
-                if (lane < 16)
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) park[(c * 32 + j) * GEMM_BM + rloc] = ok ? __uint_as_float(v[j]) : 0.f;
+                for (int j = 0; j < 32; ++j) park[(c * 32 + j + wrow) & 63] = ok ? __uint_as_float(v[j]) : 0.f;
             }
         }
     }
     __syncwarp();
     cluster_sync_all();
-    if (warp >= 2 && !*s_abort) cluster_reduce_store<EPI>(p, tiles, S, min(64, p.M), 0, n0, (int)threadIdx.x - 64, Q4K_THREADS - 64);
+    if (warp >= 2 && !*s_abort) cluster_reduce_store<EPI, GEMM_BN, true>(p, tiles, S, min(64, p.M), 0, n0, (int)threadIdx.x - 64, Q4K_THREADS - 64);
     __syncwarp();
     cluster_sync_all();
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 1) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(128u) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(Q4K_TMEM_COLS) : "memory");
     }
 }
 
