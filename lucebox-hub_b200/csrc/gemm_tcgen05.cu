@@ -532,7 +532,8 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
 //               super-block row per request: HBM sees contiguous 144-byte pieces, never 16- or 32-byte ones); its own
 //               warp so that the raw ring runs its full depth ahead of the dequantisation
 //   warps 2-17  dequantise from the raw ring into tensor memory: warp w owns the lanes 32 (w % 4) .. + 31 (the only ones
-//               it may touch), thread = one weight row; per k-step it converts 32 weights (two 8-column tcgen05.st)
+//               it may touch), thread = one weight row; eight warps take the even k-steps, eight the odd ones, a thread
+//               converting one 64-weight group (four 8-column tcgen05.st) per super-block
 //   warp 1      MMA issue: 8 x (M128 N<=64 K16) per k-step once both operands of the stage are there
 //   warps 2-5   epilogue afterwards (park, cluster reduce, store); the accumulator is [weight row][token]
 // The weight operand is value = fma_bf16(q, bf16(d*sc), -bf16(dmin*m)), two weights per instruction: the published f32
@@ -596,7 +597,7 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
         asm volatile("prefetch.tensormap [%0];" ::"l"(&tmA) : "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(&tmW) : "memory");
         *s_abort = 0;
-        for (int i = 0; i < STAGES; ++i) { g_mbar_init(fulla0 + 8 * i, 1); g_mbar_init(fullb0 + 8 * i, Q4K_DQ_WARPS); g_mbar_init(empty0 + 8 * i, 1); }
+        for (int i = 0; i < STAGES; ++i) { g_mbar_init(fulla0 + 8 * i, 1); g_mbar_init(fullb0 + 8 * i, Q4K_DQ_WARPS / 2); g_mbar_init(empty0 + 8 * i, 1); }
         for (int i = 0; i < RS; ++i) { g_mbar_init(fullr0 + 8 * i, 1); g_mbar_init(emptyr0 + 8 * i, Q4K_DQ_WARPS); }
         g_mbar_init(tfull, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -677,53 +678,55 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
             umma_commit(tfull);
         }
     } else {
-        // ---- dequantisation: thread (row, h, part) converts half of group 2*par + h of k-step `par` of every super-block
-        // (16 nibble bytes = 32 weights: chunks 2*part, 2*part+1 from the low nibbles, 4+2*part, 5+2*part from the high
-        // ones).  The loop runs per super-block with the k-step parity known at compile time: the 6-bit scale decoding
-        // is branch-free, the header is read once for both k-steps, and ring positions advance by counters. ----
-        const int dw = warp - 2, row = (warp & 3) * 32 + lane, h = (dw >> 2) & 1, part = dw >> 3;
+        // ---- dequantisation: thread (row, h, par) converts group g = 2*par + h of every super-block (32 nibble bytes = 64
+        // weights = slab h of k-step `par`): half of the warps work on the even k-steps, half on the odd ones, so the 6-bit
+        // scales of a group are decoded once and a warp meets the barriers once per 64 weights. ----
+        const int dw = warp - 2, row = (warp & 3) * 32 + lane, h = (dw >> 2) & 1, par = dw >> 3;
         const int sh = 16 * h;
-        // this thread's 32 weights of a k-step: k = 64 h + 16 part + 0..15 (low nibbles) and 64 h + 32 + 16 part + 0..15 (high)
-        const uint32_t wdst = tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(32 * h + 8 * part);
-        const unsigned char* const rbase = rawring_ptr + row * 144;
+        // slab h of the stage: columns 32 h + k / 2; the low nibbles are k = 0..31 of the slab, the high ones k = 32..63
+        const uint32_t wdst = tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(32 * h);
+        const unsigned char* const rbase = rawring_ptr + row * 144 + 16 + 32 * (2 * par + h);
         const __nv_bfloat162 k128 = __float2bfloat162_rn(128.0f);
-        int st = 0, rs = 0;
-        uint32_t st_par = 1, rs_par = 0;
+        int rs = 0;
+        uint32_t rs_par = 0;
         const int nsb = sb_end - sb_begin;
         bool alive = true;
         for (int j = 0; j < nsb && alive; ++j) {
             alive = __all_sync(0xffffffffu, g_mbar_wait(fullr0 + 8 * rs, rs_par, p.err, s_abort));
             if (!alive) break;
-            const unsigned char* rb = rbase + rs * Q4K_RAW_BYTES;
+            const unsigned char* rb = rawring_ptr + row * 144 + rs * Q4K_RAW_BYTES;
             const uint4 hd = *reinterpret_cast<const uint4*>(rb);
+            const uint4 qa = *reinterpret_cast<const uint4*>(rbase + rs * Q4K_RAW_BYTES);
+            const uint4 qb = *reinterpret_cast<const uint4*>(rbase + rs * Q4K_RAW_BYTES + 16);
             const __half2 dd = *reinterpret_cast<const __half2*>(&hd.x);
             const float d = __low2float(dd), ndmin = -__high2float(dd);
             const uint32_t sx = hd.y >> sh, sy = hd.z >> sh, sz = hd.w >> sh;      // scale bytes 2h.., 4+2h.., 8+2h..
+            uint32_t sc0, mn0, sc1, mn1;                                            // sub-blocks 2g and 2g+1 of group g = 2*par + h
+            if (par == 0) {
+                sc0 = sx & 63u; sc1 = (sx >> 8) & 63u; mn0 = sy & 63u; mn1 = (sy >> 8) & 63u;
+            } else {
+                sc0 = (sz & 0xFu) | ((sx >> 2) & 0x30u);         mn0 = ((sz >> 4) & 0xFu) | ((sy >> 2) & 0x30u);
+                sc1 = ((sz >> 8) & 0xFu) | ((sx >> 10) & 0x30u); mn1 = ((sz >> 12) & 0xFu) | ((sy >> 10) & 0x30u);
+            }
+            // operand value = bf16 fma(q, bf16(d*sc), -bf16(dmin*m)): d*sc and dmin*m are exact in f32 (11 + 6 bits), one
+            // rounding each to bf16 (round-to-nearest is symmetric, so the sign goes in before it), then one fused rounding
+            const __nv_bfloat162 ds0 = __float2bfloat162_rn(__fmul_rn(d, (float)sc0)), ds1 = __float2bfloat162_rn(__fmul_rn(d, (float)sc1));
+            const __nv_bfloat162 nm0 = __float2bfloat162_rn(__fmul_rn(ndmin, (float)mn0)), nm1 = __float2bfloat162_rn(__fmul_rn(ndmin, (float)mn1));
+            const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+            const int i = 2 * j + par, st = i % STAGES;                            // this warp's k-step and its stage
+            alive = __all_sync(0xffffffffu, g_mbar_wait(empty0 + 8 * st, ((i / STAGES) & 1) ^ 1, p.err, s_abort));
+            if (!alive) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");       // the MMAs that read this stage are done
 #pragma unroll
-            for (int par = 0; par < 2; ++par) {
-                alive = __all_sync(0xffffffffu, g_mbar_wait(empty0 + 8 * st, st_par, p.err, s_abort));
-                if (!alive) break;
-                const uint4 qv = *reinterpret_cast<const uint4*>(rb + 16 + 32 * (2 * par + h) + 16 * part);
-                uint32_t sc0, mn0, sc1, mn1;                                        // sub-blocks 2g and 2g+1 of group g = 2*par + h
-                if (par == 0) {
-                    sc0 = sx & 63u; sc1 = (sx >> 8) & 63u; mn0 = sy & 63u; mn1 = (sy >> 8) & 63u;
-                } else {
-                    sc0 = (sz & 0xFu) | ((sx >> 2) & 0x30u);         mn0 = ((sz >> 4) & 0xFu) | ((sy >> 2) & 0x30u);
-                    sc1 = ((sz >> 8) & 0xFu) | ((sx >> 10) & 0x30u); mn1 = ((sz >> 12) & 0xFu) | ((sy >> 10) & 0x30u);
-                }
-                // operand value = bf16 fma(q, bf16(d*sc), -bf16(dmin*m)): d*sc and dmin*m are exact in f32 (11 + 6 bits), one
-                // rounding each to bf16 (round-to-nearest is symmetric, so the sign goes in before it), then one fused rounding
-                const __nv_bfloat162 ds0 = __float2bfloat162_rn(__fmul_rn(d, (float)sc0)), ds1 = __float2bfloat162_rn(__fmul_rn(d, (float)sc1));
-                const __nv_bfloat162 nm0 = __float2bfloat162_rn(__fmul_rn(ndmin, (float)mn0)), nm1 = __float2bfloat162_rn(__fmul_rn(ndmin, (float)mn1));
-                const uint32_t w[4] = {qv.x, qv.y, qv.z, qv.w};
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");   // the MMAs that read this stage are done
+            for (int hi = 0; hi < 2; ++hi) {                        // 32 weights from the low nibbles, then 32 from the high ones
+                const __nv_bfloat162 dsx = hi ? ds1 : ds0, nmx = hi ? nm1 : nm0;
 #pragma unroll
-                for (int hi = 0; hi < 2; ++hi) {                    // 16 weights from the low nibbles, then 16 from the high ones
-                    const __nv_bfloat162 dsx = hi ? ds1 : ds0, nmx = hi ? nm1 : nm0;
+                for (int half = 0; half < 2; ++half) {
                     uint32_t o[8];
 #pragma unroll
                     for (int h2 = 0; h2 < 4; ++h2) {
-                        const uint32_t nib = (hi ? (w[h2] >> 4) : w[h2]) & 0x0F0F0F0Fu;
+                        const uint32_t word = w[4 * half + h2];
+                        const uint32_t nib = (hi ? (word >> 4) : word) & 0x0F0F0F0Fu;
                         // bytes (q, 0x43) are the bf16 numbers 128 + q: exact, no integer conversion
                         const uint32_t u01 = __byte_perm(nib, 0x43004300u, 0x7150), u23 = __byte_perm(nib, 0x43004300u, 0x7352);
                         const __nv_bfloat162 x01 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&u01), k128);
@@ -732,16 +735,15 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
                         o[2 * h2] = *reinterpret_cast<const uint32_t*>(&y01);
                         o[2 * h2 + 1] = *reinterpret_cast<const uint32_t*>(&y23);
                     }
-                    tmem_st8(wdst + (uint32_t)(st * (int)Q4K_W_COLS + 16 * hi), o);     // columns = k / 2, the pair's first weight in the low half
+                    tmem_st8(wdst + (uint32_t)(st * (int)Q4K_W_COLS + 16 * hi + 8 * half), o);   // the pair's first weight in the low half
                 }
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) {
-                    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(fullb0 + 8 * st) : "memory");
-                    if (par == 1) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(emptyr0 + 8 * rs) : "memory");   // super-block consumed
-                }
-                if (++st == STAGES) { st = 0; st_par ^= 1u; }
+            }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(fullb0 + 8 * st) : "memory");
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(emptyr0 + 8 * rs) : "memory");   // this warp is done with the super-block
             }
             if (++rs == RS) { rs = 0; rs_par ^= 1u; }
         }
