@@ -534,22 +534,26 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
 //   warps 2-17  dequantise from the raw ring into tensor memory: warp w owns the lanes 32 (w % 4) .. + 31 (the only ones
 //               it may touch), thread = one weight row; eight warps take the even k-steps, eight the odd ones, a thread
 //               converting one 64-weight group (four 8-column tcgen05.st) per super-block
-//   warp 1      MMA issue: 8 x (M128 N<=64 K16) per k-step once both operands of the stage are there
+//   warps 1, 19 MMA issue: 8 x (M128 N<=64 K16) per k-step once both operands of the stage are there.  Two issuing
+//               threads, one for the even k-steps and one for the odd ones, each with an accumulator of its own (the
+//               epilogue adds them): with the operands ready, ONE thread needs ~0.5 us per k-step to get its barrier
+//               observations and 8 instructions through, and the whole main loop ran at that pace; two threads took the
+//               27B tree verify from 12.0 to 10.5 ms
 //   warps 2-5   epilogue afterwards (park, cluster reduce, store); the accumulator is [weight row][token]
 // The weight operand is value = fma_bf16(q, bf16(d*sc), -bf16(dmin*m)), two weights per instruction: the published f32
 // dequantisation (d*sc)*q - dmin*m followed by a rounding to bf16 cost ~10 instructions per weight on the CUDA cores.
 // qwen35_b200_dequant_q4k keeps the published arithmetic bit for bit.  (An f16 weight operand beside bf16 activations
 // is not an option: kind::f16 with different A and B formats raised "illegal instruction" on this GPU.)
-constexpr int Q4K_THREADS = 608;                                                      // 2 + 16 dequantisation warps + the raw producer
+constexpr int Q4K_THREADS = 640;                                // 2 + 16 dequantisation warps + the raw producer + the second MMA issuer
 constexpr int Q4K_DQ_WARPS = 16;
-constexpr int Q4K_RAW_WARP = 2 + Q4K_DQ_WARPS;
+constexpr int Q4K_RAW_WARP = 2 + Q4K_DQ_WARPS, Q4K_MMA2_WARP = Q4K_RAW_WARP + 1;
 constexpr int Q4K_STAGES = 4, Q4K_RAW_STAGES = 3;
 constexpr uint32_t Q4K_X_SLAB = 64 * 128;                                              // bytes: 64 token rows x 64 k
 constexpr uint32_t Q4K_STAGE_BYTES = 2 * Q4K_X_SLAB;                                  // 16 KB of activations per 128-wide k-step
 constexpr uint32_t Q4K_RAW_BYTES = 128 * 144;                                          // one super-block per tile row
-// tensor memory: per stage 64 columns of weights (128 k as bf16 pairs), then the f32 accumulator [128 weights][64 tokens]
+// tensor memory: per stage 64 columns of weights (128 k as bf16 pairs), then two f32 accumulators [128 weights][64 tokens]
 constexpr uint32_t Q4K_W_COLS = 64, Q4K_D_COL = Q4K_STAGES * Q4K_W_COLS, Q4K_TMEM_COLS = 512;
-static_assert(Q4K_D_COL + 64 <= Q4K_TMEM_COLS, "tensor memory budget");
+static_assert(Q4K_D_COL + 2 * 64 <= Q4K_TMEM_COLS, "tensor memory budget");
 __device__ __forceinline__ uint32_t q4k_idesc(int n_tokens) {      // D f32, A and B bf16, M = 128 weight rows, N = tokens rounded up to 16
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n_tokens >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
@@ -599,7 +603,7 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
         *s_abort = 0;
         for (int i = 0; i < STAGES; ++i) { g_mbar_init(fulla0 + 8 * i, 1); g_mbar_init(fullb0 + 8 * i, Q4K_DQ_WARPS / 2); g_mbar_init(empty0 + 8 * i, 1); }
         for (int i = 0; i < RS; ++i) { g_mbar_init(fullr0 + 8 * i, 1); g_mbar_init(emptyr0 + 8 * i, Q4K_DQ_WARPS); }
-        g_mbar_init(tfull, 1);
+        g_mbar_init(tfull, 2);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
@@ -656,10 +660,12 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
                 }
             }
         }
-    } else if (warp == 1) {
+    } else if (warp == 1 || warp == Q4K_MMA2_WARP) {
         if (lane == 0) {
             const uint32_t idesc = q4k_idesc(min(64, max(16, (p.M + 15) & ~15)));
-            for (int i = 0; i < nk2; ++i) {
+            const int who = (warp == 1) ? 0 : 1;                  // k-steps who, who + 2, ... into accumulator `who` (nk2 is even)
+            const uint32_t acc = tmem_base + Q4K_D_COL + 64u * (uint32_t)who;
+            for (int i = who; i < nk2; i += 2) {
                 const int st = i % STAGES;
                 if (!g_mbar_wait(fulla0 + 8 * st, (i / STAGES) & 1, p.err, s_abort)) break;
                 if (!g_mbar_wait(fullb0 + 8 * st, (i / STAGES) & 1, p.err, s_abort)) break;
@@ -670,8 +676,7 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
                     const uint64_t xdesc = make_smem_desc(x_addr + sl * Q4K_X_SLAB);
 #pragma unroll
                     for (int k = 0; k < 4; ++k)      // 16 k = 8 columns of the weight operand, 32 bytes of the activation rows
-                        umma_bf16_ts(tmem_base + Q4K_D_COL, w_col + (uint32_t)(sl * 32 + k * 8), xdesc + (uint64_t)(2 * k), idesc,
-                                     (i > 0 || sl > 0 || k > 0) ? 1u : 0u);
+                        umma_bf16_ts(acc, w_col + (uint32_t)(sl * 32 + k * 8), xdesc + (uint64_t)(2 * k), idesc, (i > who || sl > 0 || k > 0) ? 1u : 0u);
                 }
                 umma_commit(empty0 + 8 * st);
             }
@@ -760,8 +765,12 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
                 if (c * 32 >= p.M) break;                               // tokens that do not exist are never read back
                 uint32_t v[32];
                 if (ok) {
+                    uint32_t v2[32];
                     tmem_ld32(tmem_base + Q4K_D_COL + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(c * 32), v);
+                    tmem_ld32(tmem_base + Q4K_D_COL + 64u + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(c * 32), v2);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(v2[j]));
                 }
 #pragma unroll
                 for (int j = 0; j < 32; ++j) park[(c * 32 + j + wrow) & 63] = ok ? __uint_as_float(v[j]) : 0.f;
