@@ -128,6 +128,13 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8])
     asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
                  ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]) : "memory");
 }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr) : "memory");
+}
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
@@ -539,7 +546,7 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
 //               epilogue adds them): with the operands ready, ONE thread needs ~0.5 us per k-step to get its barrier
 //               observations and 8 instructions through, and the whole main loop ran at that pace; two threads took the
 //               27B tree verify from 12.0 to 10.5 ms
-//   warps 2-5   epilogue afterwards (park, cluster reduce, store); the accumulator is [weight row][token]
+//   warps 2-17  epilogue afterwards (park, cluster reduce, store); the accumulator is [weight row][token]
 // The weight operand is value = fma_bf16(q, bf16(d*sc), -bf16(dmin*m)), two weights per instruction: the published f32
 // dequantisation (d*sc)*q - dmin*m followed by a rounding to bf16 cost ~10 instructions per weight on the CUDA cores.
 // qwen35_b200_dequant_q4k keeps the published arithmetic bit for bit.  (An f16 weight operand beside bf16 activations
@@ -752,36 +759,39 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
             }
             if (++rs == RS) { rs = 0; rs_par ^= 1u; }
         }
-        if (warp < 6) {
-            // ---- epilogue part 1: park the f32 tile column-major in the idle stage buffers ----
+        {
+            // ---- epilogue part 1: park the f32 tile in the idle stage buffers; the four warps of a lane quarter take 16
+            // tokens each ----
             const int wrow = (warp & 3) * 32 + lane;                    // this thread's weight row = its tensor-memory lane
+            const int tok0 = (dw >> 2) * 16;
             const bool ok = __all_sync(0xffffffffu, g_mbar_wait(tfull, 0, p.err, s_abort) && !*s_abort);
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             // [weight row of the tile][token], the tokens of row w rotated by w so that a warp's stores (32 rows, one token)
             // fall into 32 different banks; cluster_reduce_store<.., true> undoes the rotation
             float* park = reinterpret_cast<float*>(tiles_ptr) + wrow * GEMM_BM;
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                if (c * 32 >= p.M) break;                               // tokens that do not exist are never read back
-                uint32_t v[32];
+            if (tok0 < p.M) {                                           // tokens that do not exist are never read back
+                uint32_t v[16];
                 if (ok) {
-                    uint32_t v2[32];
-                    tmem_ld32(tmem_base + Q4K_D_COL + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(c * 32), v);
-                    tmem_ld32(tmem_base + Q4K_D_COL + 64u + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(c * 32), v2);
+                    uint32_t v2[16];
+                    const uint32_t src = tmem_base + Q4K_D_COL + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)tok0;
+                    tmem_ld16(src, v);
+                    tmem_ld16(src + 64u, v2);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(v2[j]));
+                    for (int j = 0; j < 16; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(v2[j]));
                 }
 #pragma unroll
-                for (int j = 0; j < 32; ++j) park[(c * 32 + j + wrow) & 63] = ok ? __uint_as_float(v[j]) : 0.f;
+                for (int j = 0; j < 16; ++j) park[(tok0 + j + wrow) & 63] = ok ? __uint_as_float(v[j]) : 0.f;
             }
         }
     }
     __syncwarp();
-    cluster_sync_all();
+    // every thread of every CTA of the cluster passes these barriers, whatever happened above; a CTA on its own (no split)
+    // needs neither the cluster's barrier nor the second one (nobody else reads its tile)
+    if (S > 1) cluster_sync_all(); else __syncthreads();
     if (warp >= 2 && !*s_abort) cluster_reduce_store<EPI, GEMM_BN, true>(p, tiles, S, min(64, p.M), 0, n0, (int)threadIdx.x - 64, Q4K_THREADS - 64);
     __syncwarp();
-    cluster_sync_all();
+    if (S > 1) cluster_sync_all();
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 1) {
