@@ -248,6 +248,24 @@ __device__ __forceinline__ void cluster_reduce_store(const GemmParams& p, uint32
     }
 }
 
+// The same store pass for a CTA on its own (no split): its tile is read with plain shared-memory loads (a
+// ld.shared::cluster round trip costs several times more, and the SiLU form makes two of them in a row).  Layout as
+// cluster_reduce_store<.., true> reads it: [column][GEMM_BM], the rows of column c rotated by c.
+template <int EPI, int BN>
+__device__ __forceinline__ void rotated_tile_store(const GemmParams& p, const float* park, int rows, int m0, int n0, int t, int nt) {
+    constexpr int BN_OUT = (EPI == EPI_SILU_MUL) ? BN / 2 : BN;
+    for (int item = t; item < rows * (BN_OUT / 8); item += nt) {
+        const int r = item % rows, col = (item / rows) * 8;
+        float g[8], u[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            g[e] = park[(col + e) * GEMM_BM + ((r + col + e) & 63)];
+            u[e] = (EPI == EPI_SILU_MUL) ? park[(BN / 2 + col + e) * GEMM_BM + ((r + BN / 2 + col + e) & 63)] : 0.f;
+        }
+        epilogue_store8<EPI>(p, m0 + r, n0 + col, g, u);
+    }
+}
+
 __device__ __forceinline__ float4 ld_smem4(uint32_t addr) {
     float4 v;
     asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr) : "memory");
@@ -789,7 +807,10 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
     // every thread of every CTA of the cluster passes these barriers, whatever happened above; a CTA on its own (no split)
     // needs neither the cluster's barrier nor the second one (nobody else reads its tile)
     if (S > 1) cluster_sync_all(); else __syncthreads();
-    if (warp >= 2 && !*s_abort) cluster_reduce_store<EPI, GEMM_BN, true>(p, tiles, S, min(64, p.M), 0, n0, (int)threadIdx.x - 64, Q4K_THREADS - 64);
+    if (warp >= 2 && !*s_abort) {
+        if (S > 1) cluster_reduce_store<EPI, GEMM_BN, true>(p, tiles, S, min(64, p.M), 0, n0, (int)threadIdx.x - 64, Q4K_THREADS - 64);
+        else rotated_tile_store<EPI, GEMM_BN>(p, reinterpret_cast<const float*>(tiles_ptr), min(64, p.M), 0, n0, (int)threadIdx.x - 64, Q4K_THREADS - 64);
+    }
     __syncwarp();
     if (S > 1) cluster_sync_all();
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
