@@ -582,7 +582,12 @@ static_assert(Q4K_D_COL + 2 * 64 <= Q4K_TMEM_COLS, "tensor memory budget");
 __device__ __forceinline__ uint32_t q4k_idesc(int n_tokens) {      // D f32, A and B bf16, M = 128 weight rows, N = tokens rounded up to 16
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n_tokens >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
-constexpr uint32_t Q4K_SMEM = Q4K_STAGES * Q4K_STAGE_BYTES + Q4K_RAW_STAGES * Q4K_RAW_BYTES + 1024 + 256;
+constexpr uint32_t Q4K_SMEM_USED = Q4K_STAGES * Q4K_STAGE_BYTES + Q4K_RAW_STAGES * Q4K_RAW_BYTES + 1024 + 256;
+// The CTA takes all 512 tensor-memory columns of its SM, so no other tensor-memory kernel may share the SM with it: a CTA of
+// another stream's GEMM that blocks in tcgen05.alloc beside it while its own cluster waits for it at a cluster barrier could
+// close a cycle with this kernel's cluster (tree verify runs a small bf16 GEMM beside a Q4_K projection).  Asking for 200 KB
+// of shared memory leaves room for no kernel of this library that allocates tensor memory (the smallest needs 49 KB).
+constexpr uint32_t Q4K_SMEM = Q4K_SMEM_USED > 200u * 1024u ? Q4K_SMEM_USED : 200u * 1024u;
 static_assert(Q4K_STAGES * Q4K_STAGE_BYTES >= GEMM_BM * GEMM_BN * 4, "the parked f32 tile reuses the stage buffers");
 
 __device__ __forceinline__ void q4k_scale_min_u32(uint32_t s0, uint32_t s1, uint32_t s2, int j, float& sc, float& mn) {
