@@ -258,5 +258,9 @@ __device__ __forceinline__ void bulk_load_1d(uint32_t dst, const void* src, uint
 // the kernel before it in the stream is still draining; it must call this before it reads or writes anything that
 // kernel touches.  Without the attribute the instruction returns at once.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel of the stream be scheduled now instead of when this grid's last block exits: its blocks run whatever
+// they do in front of their own pdl_wait() (set-up, loads of constant weights) beside this grid.  Only for small kernels
+// whose blocks are all resident at once: a waiting successor holds shared and tensor memory.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 }  // namespace q35

@@ -643,11 +643,15 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem_base = *tmem_slot;
-    pdl_wait();      // barriers, TMEM and tensor maps are set up; from here on the kernel touches its predecessor's outputs
+    // No pdl_wait() here: the weights are constants, so the raw producer and the dequantisation warps start at once and have
+    // the first stages of weights in tensor memory while the kernel in front of this one is still running (when that kernel
+    // lets its successor in early).  What the predecessor writes is touched only behind a pdl_wait(): the activation loads
+    // below, and the store pass (every thread waits in front of it).
 
     if (warp == 0) {
         // activation tiles: k-step i may be issued as soon as the MMAs of k-step i - STAGES have read the stage
         if (lane == 0) {
+            pdl_wait();
             int issued_a = 0;
             for (int i = 0; i < nk2; ++i) {
                 const int st = i % STAGES;
@@ -808,6 +812,7 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
         }
     }
     __syncwarp();
+    pdl_wait();
     // every thread of every CTA of the cluster passes these barriers, whatever happened above; a CTA on its own (no split)
     // needs neither the cluster's barrier nor the second one (nobody else reads its tile)
     if (S > 1) cluster_sync_all(); else __syncthreads();

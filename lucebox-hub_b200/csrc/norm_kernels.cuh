@@ -22,6 +22,7 @@ static __global__ void __launch_bounds__(256) tv_rmsnorm_kernel(const bf16* __re
     // H is a multiple of 256; a thread keeps its (up to 4) 8-element pieces of the row in registers between the two passes
     __shared__ float red[8];
     constexpr int MAXV = 4;
+    pdl_trigger();      // the projection GEMM that follows loads and dequantises its first weights beside this kernel
     pdl_wait();
     const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)blockIdx.x * H);
     const int nv = H / 8;

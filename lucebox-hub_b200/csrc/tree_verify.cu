@@ -499,6 +499,7 @@ __global__ void __launch_bounds__(TV_PV_THREADS, 1) tv_att_pv_kernel(const unsig
 // sum of the chunk partials in chunk order, times sigmoid(gate), one rounding to bf16.  grid (nodes, q_heads), 128 threads
 __global__ void __launch_bounds__(128) tv_att_merge_kernel(const float* __restrict__ partial, const bf16* __restrict__ proj, int ldp, TvDims D,
                                                            int n_nodes, int n_chunks, bf16* __restrict__ out) {
+    pdl_trigger();      // the projection GEMM that follows loads and dequantises its first weights beside this kernel
     pdl_wait();
     const int t = blockIdx.x, hq = blockIdx.y, tid = threadIdx.x;
     const int gqa = D.q_heads / D.kv_heads, R = n_nodes * gqa, kvh = hq / gqa, r = t * gqa + hq % gqa;
@@ -665,6 +666,7 @@ __global__ void __launch_bounds__(128) tv_dn_tree_kernel(const float* __restrict
 // gated norm: y = bf16(o * rsqrt(mean o^2 + eps) * w * silu(z)).  grid (nodes, v_heads), 128 threads
 __global__ void __launch_bounds__(128) tv_dn_gated_norm_kernel(const float* __restrict__ core, const bf16* __restrict__ proj, int ldp, int z_off,
                                                                const float* __restrict__ w, TvDims D, bf16* __restrict__ out) {
+    pdl_trigger();      // the projection GEMM that follows loads and dequantises its first weights beside this kernel
     pdl_wait();
     __shared__ float red[4];
     const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
