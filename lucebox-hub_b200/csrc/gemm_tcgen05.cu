@@ -643,6 +643,7 @@ gemm_q4k_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem_base = *tmem_slot;
+    pdl_trigger();
     // No pdl_wait() here: the weights are constants, so the raw producer and the dequantisation warps start at once and have
     // the first stages of weights in tensor memory while the kernel in front of this one is still running (when that kernel
     // lets its successor in early).  What the predecessor writes is touched only behind a pdl_wait(): the activation loads
