@@ -410,6 +410,7 @@ __global__ void __launch_bounds__(128) bd_att_pv_kernel(const __grid_constant__ 
 __global__ void __launch_bounds__(256) bd_att_merge_kernel(const float* __restrict__ partial, const int* __restrict__ positions,
                                                            const bf16* __restrict__ proj, int ldp, bf16* __restrict__ out, int B, int max_slices,
                                                            int n_slices, int max_ctx) {
+    pdl_trigger();      // the out-projection GEMM loads its first weight tiles beside this kernel
     pdl_wait();
     const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (gw >= B * FA_Q_HEADS) return;
@@ -597,13 +598,14 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
     // a step is ~300 dependent launches (replayed as a CUDA graph): programmatic dependent launch lets each kernel be
     // scheduled while its predecessor drains; every kernel of the step starts with pdl_wait()
     PdlGuard pdl_guard;
+    PdlEarlyGuard pdl_early;      // short kernels in front of every GEMM: weight tiles are under way before the inputs exist
     int i_dn = 0, i_fa = 0;
     for (int layer = 0; layer < n_layers; ++layer) {
         const LayerRec& L = layers_h[layer];
         const PrefillFusedB& F = fused_h[layer];
         if (layer > 0 && in->dbg_teacher)
             Q35_CUDA_OK(pdl_launch(bd_copy_rows_kernel, (int)((n_hidden / 8 + 255) / 256), 256, 0, stream, (const bf16*)in->dbg_teacher + (size_t)layer * n_hidden, hidden, (int)(n_hidden / 8)));
-        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, B, 128, 0, stream, layer == 0 ? in->tokens_in : nullptr, (const bf16*)in->embed_weight, hidden, (const bf16*)L.p[0],
+        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel<true>, B, 128, 0, stream, layer == 0 ? in->tokens_in : nullptr, (const bf16*)in->embed_weight, hidden, (const bf16*)L.p[0],
                                                  layer == 0 ? hidden : nullptr, normed, B, (uint8_t*)nullptr, (uint8_t*)nullptr));
         const bf16 *w_out, *w_post, *w_down;
         if (L.type == 0) {
@@ -614,7 +616,7 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
             Q35_CUDA_OK(pdl_launch(bd_dn_step_kernel, dim3(B, DN_HEADS, DN_V / BD_DN_ROWS), 256, 0, stream, proj, ldp, (const bf16*)L.p[DN_CONV], (const bf16*)L.p[DN_ALOG],
                                                                                   (const bf16*)L.p[DN_DTBIAS], conv, conv_stride, state, state_stride, core));
             Q35_CUDA_OK(pdl_launch(bd_conv_shift_kernel, (B * DN_CONV_CH + 255) / 256, 256, 0, stream, proj, ldp, conv, conv_stride, B));
-            Q35_CUDA_OK(pdl_launch(pf_gated_norm_kernel, (B * DN_HEADS + 15) / 16, 256, 0, stream, core, proj, ldp, (const bf16*)L.p[DN_NORM], attn, B));
+            Q35_CUDA_OK(pdl_launch(pf_gated_norm_kernel<true>, (B * DN_HEADS + 15) / 16, 256, 0, stream, core, proj, ldp, (const bf16*)L.p[DN_NORM], attn, B));
             g_launches.fetch_add(3);
             w_out = (const bf16*)L.p[DN_OUT]; w_post = (const bf16*)L.p[DN_POST_NORM]; w_down = (const bf16*)L.p[DN_DOWN];
             ++i_dn;
@@ -645,14 +647,14 @@ extern "C" int qwen35_b200_decode_batched(const Qwen35BatchedArgs* in, qwen35_st
             ++i_fa;
         }
         Q35_TRYB(gemm_bf16(attn, 2048, w_out, HIDDEN, resid, HIDDEN, hidden, HIDDEN, B, HIDDEN, 2048, 1, 0, stream));
-        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, B, 128, 0, stream, nullptr, nullptr, resid, w_post, nullptr, normed, B, (uint8_t*)nullptr, (uint8_t*)nullptr));
+        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel<true>, B, 128, 0, stream, nullptr, nullptr, resid, w_post, nullptr, normed, B, (uint8_t*)nullptr, (uint8_t*)nullptr));
         Q35_TRYB(gemm_bf16(normed, HIDDEN, (const bf16*)F.gate_up_weight, 2 * INTER, mlp, INTER, nullptr, 0, B, INTER, HIDDEN, 2, INTER, stream));
         Q35_TRYB(gemm_bf16(mlp, INTER, w_down, HIDDEN, hidden, HIDDEN, resid, HIDDEN, B, HIDDEN, INTER, 1, 0, stream));
         g_launches.fetch_add(2);
         if (in->dbg_hidden)
             Q35_CUDA_OK(pdl_launch(bd_copy_rows_kernel, (int)((n_hidden / 8 + 255) / 256), 256, 0, stream, hidden, (bf16*)in->dbg_hidden + (size_t)layer * n_hidden, (int)(n_hidden / 8)));
     }
-    Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, B, 128, 0, stream, nullptr, nullptr, hidden, (const bf16*)in->final_norm_weight, nullptr, normed, B, (uint8_t*)nullptr, (uint8_t*)nullptr));
+    Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel<true>, B, 128, 0, stream, nullptr, nullptr, hidden, (const bf16*)in->final_norm_weight, nullptr, normed, B, (uint8_t*)nullptr, (uint8_t*)nullptr));
     Q35_TRYB(gemm_bf16(normed, HIDDEN, (const bf16*)in->lm_head_weight, VOCAB, logits, VOCAB, nullptr, 0, B, VOCAB, HIDDEN, 0, 0, stream));
     Q35_CUDA_OK(pdl_launch(bd_argmax_kernel, B, 1024, 0, stream, logits, in->tokens_out, in->advance_positions ? in->positions : nullptr, in->max_ctx));
     if (in->logits_out) Q35_CUDA_OK(cudaMemcpyAsync(in->logits_out, logits, n_logits * sizeof(bf16), cudaMemcpyDeviceToDevice, stream));

@@ -61,6 +61,7 @@ struct GemmParams {
     const bf16* R; int ldr; // residual (EPI_RESIDUAL)
     int up_row_offset;      // EPI_SILU_MUL: B row of "up" = up_row_offset + column
     int* err;
+    int pdl_early;          // B is a constant weight matrix: load its first tiles in front of the dependency wait, release the successor early
 };
 
 __device__ __forceinline__ uint32_t g_smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -421,21 +422,35 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem_base = *tmem_slot;
-    pdl_wait();      // barriers, TMEM and tensor maps are set up; from here on the kernel touches its predecessor's outputs
+    // Barriers, TMEM and tensor maps are set up.  What the predecessor wrote is touched only behind a pdl_wait(): by the copy
+    // thread in front of its first activation tile, and by every thread in front of the store pass.
+    if (p.pdl_early) pdl_trigger();
 
     if (warp == 0) {
         if (lane == 0) {
-            int issued = 0;
+            // weight tiles of the first ring round: constants, so they may be under way while the predecessor still runs
+            const int pre = p.pdl_early ? min(STAGES, nkb) : 0;
+            for (int i = 0; i < pre; ++i) {
+                const uint32_t b_dst = tiles + i * SB + GEMM_BM * GEMM_BK * 2;
+                g_mbar_expect_tx(full0 + 8 * i, SB);
+                g_tma_load_2d(b_dst, &tmB, (kb_begin + i) * GEMM_BK, n0, full0 + 8 * i);
+                if (B_NBOX == 2)
+                    g_tma_load_2d(b_dst + B_BOX * GEMM_BK * 2, &tmB, (kb_begin + i) * GEMM_BK, (EPI == EPI_SILU_MUL ? p.up_row_offset : B_BOX) + n0, full0 + 8 * i);
+            }
+            pdl_wait();
+            int issued = pre;
             for (int i = 0; i < nkb; ++i) {
                 const int st = i % STAGES, kb = kb_begin + i;
-                if (!g_mbar_wait(empty0 + 8 * st, ((i / STAGES) & 1) ^ 1, p.err, s_abort)) break;
                 const uint32_t a_dst = tiles + st * SB, b_dst = a_dst + GEMM_BM * GEMM_BK * 2;
-                g_mbar_expect_tx(full0 + 8 * st, SB);
+                if (i >= pre) {
+                    if (!g_mbar_wait(empty0 + 8 * st, ((i / STAGES) & 1) ^ 1, p.err, s_abort)) break;
+                    g_mbar_expect_tx(full0 + 8 * st, SB);
+                    g_tma_load_2d(b_dst, &tmB, kb * GEMM_BK, n0, full0 + 8 * st);
+                    if (B_NBOX == 2)
+                        g_tma_load_2d(b_dst + B_BOX * GEMM_BK * 2, &tmB, kb * GEMM_BK, (EPI == EPI_SILU_MUL ? p.up_row_offset : B_BOX) + n0, full0 + 8 * st);
+                }
                 g_tma_load_2d(a_dst, &tmA, kb * GEMM_BK, m0, full0 + 8 * st);
-                g_tma_load_2d(b_dst, &tmB, kb * GEMM_BK, n0, full0 + 8 * st);
-                if (B_NBOX == 2)
-                    g_tma_load_2d(b_dst + B_BOX * GEMM_BK * 2, &tmB, kb * GEMM_BK, (EPI == EPI_SILU_MUL ? p.up_row_offset : B_BOX) + n0, full0 + 8 * st);
-                issued = i + 1;
+                issued = max(issued, i + 1);
             }
             // every copy this CTA issued must have landed before it may exit (matters only after an abort)
             if (*s_abort) {
@@ -520,6 +535,7 @@ gemm_bf16_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_c
         }
     }
     __syncwarp();
+    pdl_wait();
     if (SPLIT) {
         // every thread of every CTA of the cluster passes both barriers, whatever happened above
         cluster_sync_all();
@@ -982,7 +998,7 @@ int gemm_bf16(const bf16* A, int lda, const bf16* B, int b_rows, bf16* C, int ld
             }
         }
     }
-    GemmParams p{M, N, K, C, ldc, R, ldr, up_row_offset, (int*)ws};
+    GemmParams p{M, N, K, C, ldc, R, ldr, up_row_offset, (int*)ws, g_pdl_early ? 1 : 0};
     const int nkb = K / GEMM_BK;
     const int m_tiles = (M + GEMM_BM - 1) / GEMM_BM;
     const int bn_out = (epi == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
@@ -1070,7 +1086,7 @@ int gemm_q4k(const bf16* A, int lda, const uint8_t* W, int w_rows, bf16* C, int 
         set_error("cuTensorMapEncodeTiled failed (A %p [%d x %d] ld %d; W %p [%d rows])", (const void*)A, M, K, lda, (const void*)W, w_rows);
         return QWEN35_ERR_CUDA;
     }
-    GemmParams qp{M, N, K, C, ldc, R, ldr, up_row_offset, (int*)ws};
+    GemmParams qp{M, N, K, C, ldc, R, ldr, up_row_offset, (int*)ws, 0};
     const int bn_out = (epi == EPI_SILU_MUL) ? GEMM_BN / 2 : GEMM_BN;
     const int n_tiles = (N + bn_out - 1) / bn_out, nsb = K / 256;
     // one CTA per SM: the largest split (cluster size, not necessarily a power of two) that keeps the whole grid in ONE

@@ -111,7 +111,7 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
         // input (and the residual of its mixer) from the teacher's row block instead of the previous layer's output
         const bf16* layer_in = (a.dbg_teacher && layer > 0) ? a.dbg_teacher + (size_t)layer * S * HIDDEN : a.hidden;
         // (NVFP4: the kernel packs the normalised rows as the activation operand on the way out, and the bf16 copy is not written)
-        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, fp4 ? s_pad : S, 128, 0, stream, layer == 0 ? a.token_ids : nullptr, a.embed, layer_in, (const bf16*)L.p[0],
+        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel<false>, fp4 ? s_pad : S, 128, 0, stream, layer == 0 ? a.token_ids : nullptr, a.embed, layer_in, (const bf16*)L.p[0],
                                                  layer == 0 ? a.hidden : nullptr, fp4 ? (bf16*)nullptr : a.normalized, S,
                                                  fp4 ? (uint8_t*)act_packed : (uint8_t*)nullptr, fp4 ? (uint8_t*)act_scales : (uint8_t*)nullptr));
         g_launches.fetch_add(1);
@@ -134,7 +134,7 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
             Q35_CUDA_OK(pdl_launch(pf_dn_chunk_local_kernel, dim3(nchunks, DN_HEADS), CL_THREADS, CHUNK_LOCAL_SMEM, stream, a.proj_buf2, a.beta_buf, a.alpha_buf, scratch, S, nchunks));
             Q35_CUDA_OK(pdl_launch(pf_dn_chunk_scan_kernel, dim3(DN_HEADS, DN_V / SCAN_VW), SCAN_THREADS, CHUNK_SCAN_SMEM, stream, 
                 scratch, a.dn_out_buf, a.dn_states + (size_t)i_dn * DN_HEADS * DN_V * DN_K, S, nchunks, err_word));
-            Q35_CUDA_OK(pdl_launch(pf_gated_norm_kernel, (S * DN_HEADS + 15) / 16, 256, 0, stream, a.dn_out_buf, a.proj_buf, ldp, (const bf16*)L.p[DN_NORM], a.attn_buf, S));
+            Q35_CUDA_OK(pdl_launch(pf_gated_norm_kernel<false>, (S * DN_HEADS + 15) / 16, 256, 0, stream, a.dn_out_buf, a.proj_buf, ldp, (const bf16*)L.p[DN_NORM], a.attn_buf, S));
             g_launches.fetch_add(4);
             w_out = (const bf16*)L.p[DN_OUT]; w_post = (const bf16*)L.p[DN_POST_NORM]; w_down = (const bf16*)L.p[DN_DOWN];
             ++i_dn;
@@ -161,7 +161,7 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
         }
         // output projection + residual -> residual buffer holds the hidden state after the mixer
         Q35_TRY(gemm_bf16(a.attn_buf, 2048, w_out, HIDDEN, a.residual, HIDDEN, layer_in, HIDDEN, S, HIDDEN, 2048, 1, 0, stream));
-        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, fp4 ? s_pad : S, 128, 0, stream, nullptr, nullptr, a.residual, w_post, nullptr, fp4 ? (bf16*)nullptr : a.normalized, S,
+        Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel<false>, fp4 ? s_pad : S, 128, 0, stream, nullptr, nullptr, a.residual, w_post, nullptr, fp4 ? (bf16*)nullptr : a.normalized, S,
                                                  fp4 ? (uint8_t*)act_packed : (uint8_t*)nullptr, fp4 ? (uint8_t*)act_scales : (uint8_t*)nullptr));
         g_launches.fetch_add(1);
         if (fp4) {
@@ -188,7 +188,7 @@ static int prefill_impl(const PrefillArgs& a, cudaStream_t stream) {
     // last token: final norm, LM head, arg-max
     const bf16* last = a.hidden + (size_t)(S - 1) * HIDDEN;
     if (a.hidden_out) Q35_CUDA_OK(cudaMemcpyAsync(a.hidden_out, last, HIDDEN * sizeof(bf16), cudaMemcpyDeviceToDevice, stream));
-    Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel, a.lm_packed ? 128 : 1, 128, 0, stream, nullptr, nullptr, last, a.final_norm, nullptr, a.final_normed, 1,
+    Q35_CUDA_OK(pdl_launch(pf_rmsnorm_kernel<false>, a.lm_packed ? 128 : 1, 128, 0, stream, nullptr, nullptr, last, a.final_norm, nullptr, a.final_normed, 1,
                                              a.lm_packed ? (uint8_t*)act_packed : (uint8_t*)nullptr, a.lm_packed ? (uint8_t*)act_scales : (uint8_t*)nullptr));
     const int lm_blocks = 592;
     if (a.lm_packed) {

@@ -25,10 +25,13 @@ constexpr int DN_CHUNK = 64;
 // h_out (may be null) receives the raw row; x_out (may be null) the normalised row.  With q_packed / q_scales the normalised
 // row is also packed as the NVFP4 activation operand of the GEMM that follows (a block of 16 elements is two threads; the
 // grid then covers the rows up to the next multiple of 128, and the rows from S on are written as zeros).
+// EARLY (decode steps: a handful of blocks in front of a GEMM): the GEMM is let in at once and loads weights beside this kernel
+template <bool EARLY = false>
 static __global__ void __launch_bounds__(128) pf_rmsnorm_kernel(const int* __restrict__ ids, const bf16* __restrict__ embed,
                                                          const bf16* __restrict__ h_in, const bf16* __restrict__ w,
                                                          bf16* __restrict__ h_out, bf16* __restrict__ x_out, int S,
                                                          uint8_t* __restrict__ q_packed, uint8_t* __restrict__ q_scales) {
+    if (EARLY) pdl_trigger();
     pdl_wait();
     __shared__ float red[4];
     const int t = blockIdx.x, tid = threadIdx.x;
@@ -891,8 +894,10 @@ static __global__ void __launch_bounds__(SCAN_THREADS) pf_dn_chunk_scan_kernel(c
 }
 
 // ---- gated RMSNorm of the DeltaNet output: half a warp per (token, head) -----------------------------
+template <bool EARLY = false>
 static __global__ void __launch_bounds__(256) pf_gated_norm_kernel(const bf16* __restrict__ core, const bf16* __restrict__ proj, int ldp,
                                                             const bf16* __restrict__ norm_w, bf16* __restrict__ out, int S) {
+    if (EARLY) pdl_trigger();
     pdl_wait();
     // half a warp per (token, head): 16 lanes x 8 values, 16-byte loads and stores
     const int lane = threadIdx.x & 31, l16 = lane & 15;

@@ -16,6 +16,7 @@ static std::mutex g_mu;
 static thread_local char g_err[512] = "";
 std::atomic<long long> g_launches{0};
 bool g_pdl_launch = false;
+bool g_pdl_early = false;
 
 void set_error(const char* fmt, ...) {
     va_list ap;

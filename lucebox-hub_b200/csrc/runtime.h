@@ -23,6 +23,7 @@ extern std::atomic<long long> g_launches;
 // set by a caller whose every kernel begins with pdl_wait(): the GEMM launchers then add the programmatic-stream-
 // serialization attribute to their launches (the GEMM kernels call pdl_wait() after their prologue)
 extern bool g_pdl_launch;
+extern bool g_pdl_early;      // the bf16 GEMM loads its first weight tiles in front of its dependency wait and releases its successor at its start
 
 // cudaFuncSetAttribute acts on the current device only, so a launcher's "attribute set" flag is kept per device.
 // Two host threads that race here both set the attribute, which is harmless.
@@ -57,6 +58,10 @@ static inline cudaError_t pdl_launch(void (*kernel)(KArgs...), dim3 grid, dim3 b
 struct PdlGuard {          // while alive, the GEMM launchers add the attribute too
     PdlGuard() { g_pdl_launch = true; }
     ~PdlGuard() { g_pdl_launch = false; }
+};
+struct PdlEarlyGuard {     // for passes of short kernels (a decode step, a draft forward), where the B operand is always a weight matrix
+    PdlEarlyGuard() { g_pdl_early = true; }
+    ~PdlEarlyGuard() { g_pdl_early = false; }
 };
 
 }  // namespace q35
